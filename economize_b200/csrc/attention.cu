@@ -1,0 +1,336 @@
+// Tree-masked / causal attention over the slot KV cache on the 5th-generation tensor cores.
+//
+// Replaces economize's Triton split-K decode kernel (src/economize/attention/_decode_kernels.py:110-226) and its
+// sdpa prefill path. One CTA handles 128 "packed" query rows of one (sequence b, KV head): row p is query token
+// t = p / G of query head kvh * G + p % G (G = H / H_kv), so a GQA group's heads share every K/V tile. The CTA walks
+// 128-key chunks of the cache:
+//
+//   TMA   K, V chunk [128 keys, 128 dims] (two 64-wide 128B-swizzled boxes each), double-buffered
+//   UMMA  S = Q . K^T  (M = 128 rows, N = 128 keys, K = 128 dims) into TMEM columns [0, 128)
+//   regs  thread r (TMEM lane r) reads its score row, applies the scale and the visibility rule, updates the
+//         running max / sum, and writes P = exp(s - max) as bf16 into a swizzled shared tile
+//   UMMA  PV = P . V  (N = 128 dims, V read MN-major) into TMEM columns [128, 256)
+//   regs  O = O * exp(max_old - max_new) + PV
+//
+// Visibility of slot s for query token t of row b: s < kv_len[b] (committed prefix), or j = s - kv_len[b] < n_new[b]
+// and (bit j of mask[b, t], or j <= q_offset + t without a mask). The key range may be split over `splits` CTAs,
+// whose (O, max, sum) partials a merge kernel combines in log-sum-exp form (the split-K merge of the reference).
+#include <algorithm>
+
+#include "common.cuh"
+#include "launchers.h"
+
+namespace ecz {
+
+namespace {
+
+constexpr int kRows = 128;
+constexpr int kKeys = 128;
+constexpr int kDim = 128;
+constexpr int kAtom = kRows * 128;          // bytes of one 64-column swizzled half tile (128 rows x 128 B)
+constexpr int kTile = 2 * kAtom;            // a 128 x 128 bf16 tile
+constexpr int kSmem = 6 * kTile + 1024 + 256;  // Q, P, 2 x K, 2 x V
+
+__device__ __forceinline__ void store_row_swizzled(uint8_t* tile, int r, int chunk, uint4 v) {
+  // chunk in [0, 16): 16-byte chunk of a 256-byte row; chunks 0-7 in the first half tile, 8-15 in the second
+  uint8_t* atom = tile + (chunk >> 3) * kAtom;
+  const int c = chunk & 7;
+  *reinterpret_cast<uint4*>(atom + r * 128 + ((c ^ (r & 7)) << 4)) = v;
+}
+
+__global__ void __launch_bounds__(128, 1)
+    attn_tc_kernel(const bf16* __restrict__ q, const __grid_constant__ CUtensorMap tm_k,
+                   const __grid_constant__ CUtensorMap tm_v, bf16* __restrict__ out, float* __restrict__ ws_o,
+                   float* __restrict__ ws_ml, const int* __restrict__ kv_len, const int* __restrict__ n_new,
+                   const int64_t* __restrict__ mask, int T, int H, int Hkv, int S, float scale_log2, int q_offset,
+                   int chunks_per_split, int m_tiles, unsigned* status) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* q_tile = smem;
+  uint8_t* p_tile = smem + kTile;
+  uint8_t* k_tiles = smem + 2 * kTile;
+  uint8_t* v_tiles = smem + 4 * kTile;
+  uint64_t* kv_full = reinterpret_cast<uint64_t*>(smem + 6 * kTile);
+  uint64_t* bar_s = kv_full + 2;
+  uint64_t* bar_pv = bar_s + 1;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bar_pv + 1);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+  const int tid = threadIdx.x, warp = tid >> 5;
+  const int m_tile = blockIdx.x % m_tiles;
+  const int bh = blockIdx.x / m_tiles;
+  const int b = bh / Hkv, kvh = bh % Hkv;
+  const int split = blockIdx.y, splits = gridDim.y;
+  const int G = H / Hkv;
+
+  // this thread's query row
+  const int p = m_tile * kRows + tid;
+  const int t = p / G;
+  const int head = kvh * G + p % G;
+  const bool row_valid = t < T;
+  const int base = kv_len[b];
+  const int nn = n_new[b];
+  const uint64_t bits = (row_valid && mask != nullptr) ? static_cast<uint64_t>(mask[static_cast<size_t>(b) * T + t])
+                                                       : 0ull;
+
+  // key chunks this CTA covers: up to the last slot any row of the tile may see
+  int t_last = std::min(T - 1, ((m_tile + 1) * kRows - 1) / G);
+  int visible_end = mask != nullptr ? base + nn : base + std::min(nn, q_offset + t_last + 1);
+  visible_end = std::min(visible_end, S);
+  const int n_chunks = (visible_end + kKeys - 1) / kKeys;
+  const int c0 = split * chunks_per_split;
+  const int c1 = std::min(n_chunks, c0 + chunks_per_split);
+
+  if (tid == 0) {
+    mbar_init(&kv_full[0], 1);
+    mbar_init(&kv_full[1], 1);
+    mbar_init(bar_s, 1);
+    mbar_init(bar_pv, 1);
+    *abort_flag = 0;
+    fence_mbar_init();
+  }
+  __syncwarp();
+  if (warp == 0) tmem_alloc(tmem_slot, 256);
+
+  // Q row -> swizzled K-major tile (zeros for padding rows)
+  {
+    const uint4* src = reinterpret_cast<const uint4*>(q + (static_cast<size_t>(b) * T + t) * H * kDim +
+                                                      static_cast<size_t>(head) * kDim);
+#pragma unroll
+    for (int c = 0; c < 16; ++c) store_row_swizzled(q_tile, tid, c, row_valid ? src[c] : make_uint4(0, 0, 0, 0));
+  }
+  fence_async_smem();
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+  const uint32_t tmem_s = tmem, tmem_pv = tmem + 128;
+  const uint32_t lane_off = static_cast<uint32_t>(warp * 32) << 16;
+  const size_t kv_row0 = (static_cast<size_t>(b) * Hkv + kvh) * S;
+
+  auto issue_kv = [&](int c, int s) {
+    mbar_arrive_expect_tx(&kv_full[s], 4 * kAtom);
+    const int y = static_cast<int>(kv_row0 + static_cast<size_t>(c) * kKeys);
+    tma_load_2d(k_tiles + s * kTile, &tm_k, &kv_full[s], 0, y);
+    tma_load_2d(k_tiles + s * kTile + kAtom, &tm_k, &kv_full[s], 64, y);
+    tma_load_2d(v_tiles + s * kTile, &tm_v, &kv_full[s], 0, y);
+    tma_load_2d(v_tiles + s * kTile + kAtom, &tm_v, &kv_full[s], 64, y);
+  };
+  if (tid == 0) {
+    if (c0 < c1) issue_kv(c0, 0);
+    if (c0 + 1 < c1) issue_kv(c0 + 1, 1);
+  }
+
+  float o[kDim];
+#pragma unroll
+  for (int d = 0; d < kDim; ++d) o[d] = 0.f;
+  float m_run = -INFINITY, l_run = 0.f;
+  constexpr uint32_t idesc_s = idesc_bf16_f32(kRows, kKeys);
+  constexpr uint32_t idesc_pv = idesc_bf16_f32(kRows, kDim, /*b_mn_major=*/true);
+  bool ok = true;
+
+  for (int c = c0; c < c1 && ok; ++c) {
+    const int i = c - c0;
+    const int s = i & 1;
+    const uint32_t kv_phase = (i >> 1) & 1;
+    const uint32_t ph = i & 1;
+    ok = mbar_wait(&kv_full[s], kv_phase, status, kStatusWaitFull, abort_flag);
+    if (!ok) break;
+    if (tid == 0) {
+      tc_fence_after();
+      const uint32_t qa = smem_u32(q_tile), ka = smem_u32(k_tiles + s * kTile);
+#pragma unroll
+      for (int kk = 0; kk < kDim / 16; ++kk) {
+        const uint32_t off = (kk >> 2) * kAtom + (kk & 3) * 32;
+        umma_bf16(tmem_s, desc_kmajor_sw128(qa + off), desc_kmajor_sw128(ka + off), idesc_s, kk != 0);
+      }
+      umma_commit(bar_s);
+    }
+    __syncwarp();
+    ok = mbar_wait(bar_s, ph, status, kStatusWaitAccum, abort_flag);
+    if (!ok) break;
+    __syncwarp();
+    tc_fence_after();
+
+    // pass 1: masked row max of this chunk
+    const int slot0 = c * kKeys;
+    float cmax = -INFINITY;
+#pragma unroll 1
+    for (int cc = 0; cc < kKeys; cc += 16) {
+      float v[16];
+      tmem_ld16(tmem_s + lane_off + cc, v);
+#pragma unroll
+      for (int j = 0; j < 16; ++j) {
+        const int slot = slot0 + cc + j;
+        const int jn = slot - base;
+        bool vis = row_valid && (slot < base || (jn < nn && (mask != nullptr ? (jn < 64 && ((bits >> jn) & 1ull) != 0ull)
+                                                                             : jn <= q_offset + t)));
+        if (vis) cmax = fmaxf(cmax, v[j] * scale_log2);
+      }
+    }
+    const float m_new = fmaxf(m_run, cmax);
+    const float alpha = m_new == -INFINITY ? 1.f : exp2f(m_run - m_new);
+    // pass 2: probabilities -> bf16 P tile, running sum
+    float csum = 0.f;
+#pragma unroll 1
+    for (int cc = 0; cc < kKeys; cc += 16) {
+      float v[16];
+      tmem_ld16(tmem_s + lane_off + cc, v);
+      uint32_t packed[8];
+#pragma unroll
+      for (int j = 0; j < 16; j += 2) {
+        float pr[2];
+#pragma unroll
+        for (int u = 0; u < 2; ++u) {
+          const int slot = slot0 + cc + j + u;
+          const int jn = slot - base;
+          bool vis = row_valid && (slot < base || (jn < nn && (mask != nullptr ? (jn < 64 && ((bits >> jn) & 1ull) != 0ull)
+                                                                               : jn <= q_offset + t)));
+          pr[u] = vis ? exp2f(v[j + u] * scale_log2 - m_new) : 0.f;
+        }
+        __nv_bfloat162 h2 = __floats2bfloat162_rn(pr[0], pr[1]);
+        csum += __bfloat162float(h2.x) + __bfloat162float(h2.y);  // the sum of what P . V multiplies
+        packed[j / 2] = *reinterpret_cast<uint32_t*>(&h2);
+      }
+      store_row_swizzled(p_tile, tid, cc / 8, make_uint4(packed[0], packed[1], packed[2], packed[3]));
+      store_row_swizzled(p_tile, tid, cc / 8 + 1, make_uint4(packed[4], packed[5], packed[6], packed[7]));
+    }
+    l_run = l_run * alpha + csum;
+    m_run = m_new;
+    fence_async_smem();
+    tc_fence_before();
+    __syncthreads();
+    if (tid == 0) {
+      tc_fence_after();
+      const uint32_t pa = smem_u32(p_tile), va = smem_u32(v_tiles + s * kTile);
+#pragma unroll
+      for (int kk = 0; kk < kKeys / 16; ++kk) {
+        const uint32_t a_off = (kk >> 2) * kAtom + (kk & 3) * 32;
+        umma_bf16(tmem_pv, desc_kmajor_sw128(pa + a_off), desc_mnmajor_sw128(va + kk * 2048, kAtom), idesc_pv,
+                  kk != 0);
+      }
+      umma_commit(bar_pv);
+    }
+    __syncwarp();
+    ok = mbar_wait(bar_pv, ph, status, kStatusWaitAccum, abort_flag);
+    if (!ok) break;
+    tc_fence_after();
+    if (tid == 0 && c + 2 < c1) issue_kv(c + 2, s);  // both MMAs reading stage s are done
+    __syncwarp();
+#pragma unroll
+    for (int cc = 0; cc < kDim; cc += 16) {
+      float v[16];
+      tmem_ld16(tmem_pv + lane_off + cc, v);
+#pragma unroll
+      for (int j = 0; j < 16; ++j) o[cc + j] = o[cc + j] * alpha + v[j];
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  const bool failed = *abort_flag != 0;
+
+  if (!failed && row_valid) {
+    if (splits == 1) {
+      const float inv = l_run > 0.f ? 1.f / l_run : 0.f;
+      uint4* dst = reinterpret_cast<uint4*>(out + ((static_cast<size_t>(b) * T + t) * H + head) * kDim);
+#pragma unroll
+      for (int c = 0; c < 16; ++c) {
+        uint32_t w[4];
+#pragma unroll
+        for (int u = 0; u < 4; ++u) {
+          __nv_bfloat162 h2 = __floats2bfloat162_rn(o[c * 8 + 2 * u] * inv, o[c * 8 + 2 * u + 1] * inv);
+          w[u] = *reinterpret_cast<uint32_t*>(&h2);
+        }
+        dst[c] = make_uint4(w[0], w[1], w[2], w[3]);
+      }
+    } else {
+      const size_t slot = (static_cast<size_t>(blockIdx.x) * splits + split) * kRows + tid;
+      float4* dst = reinterpret_cast<float4*>(ws_o + slot * kDim);
+#pragma unroll
+      for (int c = 0; c < kDim / 4; ++c) dst[c] = make_float4(o[4 * c], o[4 * c + 1], o[4 * c + 2], o[4 * c + 3]);
+      ws_ml[slot * 2] = m_run;
+      ws_ml[slot * 2 + 1] = l_run;
+    }
+  }
+  if (warp == 0) tmem_dealloc(tmem, 256);
+}
+
+// Combine the split partials of every packed row: out = sum_s O_s 2^(m_s - M) / sum_s l_s 2^(m_s - M).
+__global__ void __launch_bounds__(128) attn_merge_kernel(const float* __restrict__ ws_o,
+                                                         const float* __restrict__ ws_ml, bf16* __restrict__ out,
+                                                         int T, int H, int Hkv, int m_tiles, int splits) {
+  const int tile = blockIdx.x;  // (b * Hkv + kvh) * m_tiles + m_tile
+  const int r = blockIdx.y * 4 + (threadIdx.x >> 5);
+  const int lane = threadIdx.x & 31;
+  const int m_tile = tile % m_tiles, bh = tile / m_tiles;
+  const int b = bh / Hkv, kvh = bh % Hkv;
+  const int G = H / Hkv;
+  const int p = m_tile * kRows + r;
+  const int t = p / G;
+  if (t >= T) return;
+  const int head = kvh * G + p % G;
+  float mx = -INFINITY;
+  for (int s = 0; s < splits; ++s) {
+    const size_t slot = (static_cast<size_t>(tile) * splits + s) * kRows + r;
+    if (ws_ml[slot * 2 + 1] > 0.f) mx = fmaxf(mx, ws_ml[slot * 2]);
+  }
+  float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+  float denom = 0.f;
+  for (int s = 0; s < splits; ++s) {
+    const size_t slot = (static_cast<size_t>(tile) * splits + s) * kRows + r;
+    const float l = ws_ml[slot * 2 + 1];
+    if (!(l > 0.f)) continue;
+    const float w = exp2f(ws_ml[slot * 2] - mx);
+    const float4 v = reinterpret_cast<const float4*>(ws_o + slot * kDim)[lane];
+    acc.x += v.x * w; acc.y += v.y * w; acc.z += v.z * w; acc.w += v.w * w;
+    denom += l * w;
+  }
+  const float inv = denom > 0.f ? 1.f / denom : 0.f;
+  bf16* dst = out + ((static_cast<size_t>(b) * T + t) * H + head) * kDim + lane * 4;
+  *reinterpret_cast<__nv_bfloat162*>(dst) = __floats2bfloat162_rn(acc.x * inv, acc.y * inv);
+  *reinterpret_cast<__nv_bfloat162*>(dst + 2) = __floats2bfloat162_rn(acc.z * inv, acc.w * inv);
+}
+
+}  // namespace
+
+AttnPlan attention_plan(int B, int T, int H, int Hkv, int S, int num_sms) {
+  AttnPlan plan;
+  const int G = H / Hkv;
+  plan.m_tiles = (T * G + kRows - 1) / kRows;
+  const int total_chunks = (S + kKeys - 1) / kKeys;
+  const int ctas = B * Hkv * plan.m_tiles;
+  int splits = 1;
+  if (ctas < num_sms) splits = std::min(total_chunks, std::max(1, (2 * num_sms) / ctas));
+  plan.chunks_per_split = (total_chunks + splits - 1) / splits;
+  plan.splits = (total_chunks + plan.chunks_per_split - 1) / plan.chunks_per_split;
+  plan.ws_floats = plan.splits > 1 ? static_cast<long>(ctas) * plan.splits * kRows * (kDim + 2) : 0;
+  return plan;
+}
+
+int launch_attention(const void* q, const CUtensorMap* tm_k, const CUtensorMap* tm_v, void* out, float* ws,
+                     const int* kv_len, const int* n_new, const int64_t* mask, int B, int T, int H, int Hkv, int D,
+                     int S, float scale, int q_offset, const AttnPlan& plan, unsigned* status, cudaStream_t stream) {
+  if (D != kDim || H % Hkv != 0) return -1;
+  if (mask != nullptr && T > 64) return -1;
+  static bool configured = false;
+  if (!configured) {
+    cudaFuncSetAttribute(attn_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmem);
+    configured = true;
+  }
+  const int ctas = B * Hkv * plan.m_tiles;
+  float* ws_o = plan.splits > 1 ? ws : nullptr;
+  float* ws_ml = plan.splits > 1 ? ws + static_cast<size_t>(ctas) * plan.splits * kRows * kDim : nullptr;
+  dim3 grid(ctas, plan.splits);
+  attn_tc_kernel<<<grid, 128, kSmem, stream>>>(static_cast<const bf16*>(q), *tm_k, *tm_v, static_cast<bf16*>(out),
+                                               ws_o, ws_ml, kv_len, n_new, mask, T, H, Hkv, S,
+                                               scale * 1.4426950408889634f, q_offset, plan.chunks_per_split,
+                                               plan.m_tiles, status);
+  if (plan.splits > 1) {
+    dim3 mgrid(ctas, kRows / 4);
+    attn_merge_kernel<<<mgrid, 128, 0, stream>>>(ws_o, ws_ml, static_cast<bf16*>(out), T, H, Hkv, plan.m_tiles,
+                                                 plan.splits);
+  }
+  return 0;
+}
+
+}  // namespace ecz

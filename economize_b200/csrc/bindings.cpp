@@ -1,0 +1,302 @@
+// PyTorch bindings of the economize_b200 sm_100a kernels (module economize_b200._C).
+//
+// Each op checks devices, dtypes and shapes, builds the TMA descriptors it needs (cached per pointer and shape),
+// allocates outputs and workspaces through PyTorch's caching allocator (so CUDA-graph capture works) and launches
+// on the current stream. A launcher that refuses a shape raises a Python error; nothing falls back to PyTorch.
+#include <ATen/cuda/CUDAContext.h>
+#include <c10/cuda/CUDAGuard.h>
+#include <torch/extension.h>
+
+#include <cstring>
+#include <list>
+#include <mutex>
+#include <tuple>
+#include <unordered_map>
+#include <vector>
+
+#include "launchers.h"
+
+namespace {
+
+using at::Tensor;
+
+#define CHECK_CUDA(x) TORCH_CHECK((x).is_cuda(), #x " must be a CUDA tensor")
+#define CHECK_BF16(x) TORCH_CHECK((x).scalar_type() == at::kBFloat16, #x " must be bfloat16")
+#define CHECK_I32(x) TORCH_CHECK((x).scalar_type() == at::kInt, #x " must be int32")
+#define CHECK_I64(x) TORCH_CHECK((x).scalar_type() == at::kLong, #x " must be int64")
+
+int num_sms(int device) {
+  static std::vector<int> cache(64, 0);
+  if (cache[device] == 0) {
+    cudaDeviceGetAttribute(&cache[device], cudaDevAttrMultiProcessorCount, device);
+  }
+  return cache[device];
+}
+
+// Per-device status word that kernels set when a bounded wait gives up.
+unsigned* status_word(const at::Device& device) {
+  static std::mutex mu;
+  static std::unordered_map<int, Tensor> words;
+  std::lock_guard<std::mutex> lock(mu);
+  auto it = words.find(device.index());
+  if (it == words.end()) {
+    it = words.emplace(device.index(), at::zeros({1}, at::TensorOptions().dtype(at::kInt).device(device))).first;
+  }
+  return reinterpret_cast<unsigned*>(it->second.data_ptr<int>());
+}
+
+// LRU cache of tensor maps keyed by (base, rows, cols, stride, box_rows).
+struct MapKey {
+  uintptr_t base;
+  uint64_t rows, cols, stride;
+  uint32_t box;
+  bool operator==(const MapKey& o) const {
+    return base == o.base && rows == o.rows && cols == o.cols && stride == o.stride && box == o.box;
+  }
+};
+struct MapKeyHash {
+  size_t operator()(const MapKey& k) const {
+    return std::hash<uintptr_t>()(k.base) ^ (k.rows * 1315423911u) ^ (k.cols << 7) ^ (k.stride << 17) ^ k.box;
+  }
+};
+
+const CUtensorMap* tensor_map(const void* base, uint64_t rows, uint64_t cols, uint64_t stride, uint32_t box) {
+  static std::mutex mu;
+  static std::list<std::pair<MapKey, CUtensorMap>> lru;
+  static std::unordered_map<MapKey, std::list<std::pair<MapKey, CUtensorMap>>::iterator, MapKeyHash> index;
+  constexpr size_t kCap = 4096;
+  std::lock_guard<std::mutex> lock(mu);
+  MapKey key{reinterpret_cast<uintptr_t>(base), rows, cols, stride, box};
+  auto it = index.find(key);
+  if (it != index.end()) {
+    lru.splice(lru.begin(), lru, it->second);
+    return &it->second->second;
+  }
+  CUtensorMap map;
+  std::memset(&map, 0, sizeof(map));
+  const int rc = ecz::make_tmap_2d_bf16(&map, base, rows, cols, stride, box);
+  TORCH_CHECK(rc == 0, "cuTensorMapEncodeTiled failed (code ", rc, ") for rows=", rows, " cols=", cols);
+  lru.emplace_front(key, map);
+  index[key] = lru.begin();
+  if (lru.size() > kCap) {
+    index.erase(lru.back().first);
+    lru.pop_back();
+  }
+  return &lru.front().second;
+}
+
+std::tuple<Tensor, Tensor> rmsnorm(Tensor x, Tensor w, double eps, c10::optional<Tensor> resid) {
+  CHECK_CUDA(x);
+  CHECK_BF16(x);
+  CHECK_BF16(w);
+  c10::cuda::CUDAGuard guard(x.device());
+  x = x.contiguous();
+  const int hidden = static_cast<int>(x.size(-1));
+  const int rows = static_cast<int>(x.numel() / hidden);
+  Tensor r;
+  if (resid.has_value()) {
+    r = resid->contiguous();
+    CHECK_BF16(r);
+    TORCH_CHECK(r.numel() == x.numel(), "residual shape mismatch");
+  }
+  auto out = at::empty_like(x);
+  auto resid_out = at::empty_like(x);
+  const int rc = ecz::launch_rmsnorm(x.data_ptr(), resid.has_value() ? r.data_ptr() : nullptr, w.data_ptr(),
+                                     out.data_ptr(), resid_out.data_ptr(), rows, hidden, static_cast<float>(eps),
+                                     at::cuda::getCurrentCUDAStream());
+  TORCH_CHECK(rc == 0, "rmsnorm: unsupported hidden size ", hidden);
+  return {out, resid_out};
+}
+
+Tensor rope_store(Tensor qkv, Tensor positions, Tensor cos, Tensor sin, int64_t H, int64_t Hkv, int64_t D,
+                  Tensor k_cache, Tensor v_cache, Tensor kv_len, Tensor n_new, c10::optional<Tensor> q_norm,
+                  c10::optional<Tensor> k_norm, double eps, int64_t q_offset) {
+  CHECK_CUDA(qkv);
+  CHECK_BF16(qkv);
+  CHECK_BF16(k_cache);
+  CHECK_I32(positions);
+  CHECK_I32(kv_len);
+  CHECK_I32(n_new);
+  TORCH_CHECK(cos.scalar_type() == at::kFloat && sin.scalar_type() == at::kFloat, "rope tables must be fp32");
+  TORCH_CHECK(qkv.dim() == 3 && k_cache.dim() == 4, "rope_store expects qkv [B, T, W] and caches [B, Hkv, S, D]");
+  TORCH_CHECK(k_cache.is_contiguous() && v_cache.is_contiguous(), "caches must be contiguous");
+  c10::cuda::CUDAGuard guard(qkv.device());
+  qkv = qkv.contiguous();
+  positions = positions.contiguous();
+  const int B = static_cast<int>(qkv.size(0)), T = static_cast<int>(qkv.size(1));
+  TORCH_CHECK(qkv.size(2) == (H + 2 * Hkv) * D, "qkv width mismatch");
+  auto q = at::empty({B, T, H, D}, qkv.options());
+  const int rc = ecz::launch_rope_store(
+      qkv.data_ptr(), positions.data_ptr<int>(), cos.data_ptr<float>(), sin.data_ptr<float>(), q.data_ptr(),
+      k_cache.data_ptr(), v_cache.data_ptr(), kv_len.data_ptr<int>(), n_new.data_ptr<int>(),
+      q_norm.has_value() ? q_norm->data_ptr() : nullptr, k_norm.has_value() ? k_norm->data_ptr() : nullptr,
+      static_cast<float>(eps), B, T, static_cast<int>(H), static_cast<int>(Hkv), static_cast<int>(D),
+      static_cast<int>(k_cache.size(2)), static_cast<int>(q_offset), at::cuda::getCurrentCUDAStream());
+  TORCH_CHECK(rc == 0, "rope_store: unsupported head_dim ", D);
+  return q;
+}
+
+Tensor attention(Tensor q, Tensor k_cache, Tensor v_cache, Tensor kv_len, Tensor n_new, c10::optional<Tensor> mask,
+                 double scale, int64_t q_offset) {
+  CHECK_CUDA(q);
+  CHECK_BF16(q);
+  CHECK_BF16(k_cache);
+  CHECK_BF16(v_cache);
+  CHECK_I32(kv_len);
+  CHECK_I32(n_new);
+  TORCH_CHECK(q.dim() == 4 && k_cache.dim() == 4, "attention expects q [B, T, H, D] and caches [B, Hkv, S, D]");
+  TORCH_CHECK(k_cache.is_contiguous() && v_cache.is_contiguous(), "caches must be contiguous");
+  c10::cuda::CUDAGuard guard(q.device());
+  q = q.contiguous();
+  const int B = static_cast<int>(q.size(0)), T = static_cast<int>(q.size(1)), H = static_cast<int>(q.size(2)),
+            D = static_cast<int>(q.size(3));
+  const int Hkv = static_cast<int>(k_cache.size(1)), S = static_cast<int>(k_cache.size(2));
+  const int64_t* mask_ptr = nullptr;
+  Tensor m;
+  if (mask.has_value()) {
+    m = mask->contiguous();
+    CHECK_I64(m);
+    TORCH_CHECK(T <= 64, "tree masks cover at most 64 new tokens");
+    mask_ptr = m.data_ptr<int64_t>();
+  }
+  auto out = at::empty_like(q);
+  const ecz::AttnPlan plan = ecz::attention_plan(B, T, H, Hkv, S, num_sms(q.get_device()));
+  Tensor ws;
+  if (plan.ws_floats > 0) ws = at::empty({plan.ws_floats}, q.options().dtype(at::kFloat));
+  const uint64_t rows = static_cast<uint64_t>(B) * Hkv * S;
+  const CUtensorMap* tk = tensor_map(k_cache.data_ptr(), rows, D, D, 128);
+  const CUtensorMap* tv = tensor_map(v_cache.data_ptr(), rows, D, D, 128);
+  const int rc = ecz::launch_attention(q.data_ptr(), tk, tv, out.data_ptr(),
+                                       plan.ws_floats > 0 ? ws.data_ptr<float>() : nullptr, kv_len.data_ptr<int>(),
+                                       n_new.data_ptr<int>(), mask_ptr, B, T, H, Hkv, D, S,
+                                       static_cast<float>(scale), static_cast<int>(q_offset), plan,
+                                       status_word(q.device()), at::cuda::getCurrentCUDAStream());
+  TORCH_CHECK(rc == 0, "attention: unsupported shape (head_dim must be 128, H divisible by H_kv)");
+  return out;
+}
+
+Tensor silu_mul(Tensor gu) {
+  CHECK_CUDA(gu);
+  CHECK_BF16(gu);
+  c10::cuda::CUDAGuard guard(gu.device());
+  gu = gu.contiguous();
+  const int F2 = static_cast<int>(gu.size(-1));
+  const int rows = static_cast<int>(gu.numel() / F2);
+  std::vector<int64_t> shape(gu.sizes().begin(), gu.sizes().end());
+  shape.back() = F2 / 2;
+  auto out = at::empty(shape, gu.options());
+  const int rc = ecz::launch_silu_mul(gu.data_ptr(), out.data_ptr(), rows, F2 / 2, at::cuda::getCurrentCUDAStream());
+  TORCH_CHECK(rc == 0, "silu_mul: width must be a multiple of 16");
+  return out;
+}
+
+Tensor linear(Tensor x, Tensor w) {
+  CHECK_CUDA(x);
+  CHECK_BF16(x);
+  CHECK_BF16(w);
+  TORCH_CHECK(x.dim() == 2 && w.dim() == 2 && x.size(1) == w.size(1), "linear expects x [M, K] and w [N, K]");
+  c10::cuda::CUDAGuard guard(x.device());
+  x = x.contiguous();
+  w = w.contiguous();
+  const int M = static_cast<int>(x.size(0)), K = static_cast<int>(x.size(1)), N = static_cast<int>(w.size(0));
+  auto y = at::empty({M, N}, x.options());
+  if (M == 0) return y;
+  const int bn = ecz::gemm_block_n(M);
+  const int splits = ecz::gemm_splits(M, N, K, num_sms(x.get_device()));
+  Tensor ws;
+  if (splits > 1) ws = at::empty({static_cast<int64_t>(splits) * M * N}, x.options().dtype(at::kFloat));
+  const CUtensorMap* tw = tensor_map(w.data_ptr(), N, K, K, 128);
+  const CUtensorMap* tx = tensor_map(x.data_ptr(), M, K, K, bn);
+  const int rc = ecz::launch_gemm_bf16(tw, tx, y.data_ptr(), splits > 1 ? ws.data_ptr<float>() : nullptr, M, N, K,
+                                       splits, status_word(x.device()), at::cuda::getCurrentCUDAStream());
+  TORCH_CHECK(rc == 0, "linear: K must be a multiple of 8 and N of 4");
+  return y;
+}
+
+Tensor argmax(Tensor x) {
+  CHECK_CUDA(x);
+  TORCH_CHECK(x.scalar_type() == at::kBFloat16 || x.scalar_type() == at::kFloat, "argmax takes bf16 or fp32");
+  c10::cuda::CUDAGuard guard(x.device());
+  x = x.contiguous();
+  const int V = static_cast<int>(x.size(-1));
+  const int rows = static_cast<int>(x.numel() / V);
+  auto out = at::empty({rows}, x.options().dtype(at::kLong));
+  ecz::launch_argmax(x.data_ptr(), x.scalar_type() == at::kBFloat16, out.data_ptr<int64_t>(), rows, V,
+                     at::cuda::getCurrentCUDAStream());
+  return out;
+}
+
+std::tuple<Tensor, Tensor, Tensor> greedy_accept(Tensor tokens, Tensor parents, Tensor pred) {
+  CHECK_CUDA(tokens);
+  CHECK_I64(tokens);
+  CHECK_I64(parents);
+  CHECK_I64(pred);
+  c10::cuda::CUDAGuard guard(tokens.device());
+  tokens = tokens.contiguous();
+  parents = parents.contiguous();
+  pred = pred.contiguous();
+  const int B = static_cast<int>(tokens.size(0)), T = static_cast<int>(tokens.size(1));
+  auto n_acc = at::empty({B}, tokens.options().dtype(at::kInt));
+  auto path = at::empty({B, T}, tokens.options().dtype(at::kInt));
+  auto out = at::empty({B, T}, tokens.options());
+  const int rc = ecz::launch_greedy_accept(tokens.data_ptr<int64_t>(), parents.data_ptr<int64_t>(),
+                                           pred.data_ptr<int64_t>(), n_acc.data_ptr<int>(), path.data_ptr<int>(),
+                                           out.data_ptr<int64_t>(), B, T, at::cuda::getCurrentCUDAStream());
+  TORCH_CHECK(rc == 0, "greedy_accept: at most 64 tree nodes");
+  return {n_acc, path, out};
+}
+
+void kv_compact(Tensor cache, Tensor kv_len, Tensor path, Tensor n_acc) {
+  CHECK_CUDA(cache);
+  CHECK_BF16(cache);
+  CHECK_I32(kv_len);
+  CHECK_I32(path);
+  CHECK_I32(n_acc);
+  TORCH_CHECK(cache.dim() == 6 && cache.is_contiguous(), "cache must be a contiguous [L, 2, B, Hkv, S, D] tensor");
+  c10::cuda::CUDAGuard guard(cache.device());
+  path = path.contiguous();
+  const int LH = static_cast<int>(cache.size(0) * cache.size(1));
+  const int B = static_cast<int>(cache.size(2)), Hkv = static_cast<int>(cache.size(3));
+  const int S = static_cast<int>(cache.size(4)), D = static_cast<int>(cache.size(5));
+  const int T = static_cast<int>(path.size(1));
+  const int max_depth = std::max(1, T - 1);
+  const int rc = ecz::launch_kv_compact(cache.data_ptr(), kv_len.data_ptr<int>(), path.data_ptr<int>(),
+                                        n_acc.data_ptr<int>(), LH, B, Hkv, S, D, T, std::min(max_depth, 64),
+                                        at::cuda::getCurrentCUDAStream());
+  TORCH_CHECK(rc == 0, "kv_compact: unsupported head_dim or path length");
+}
+
+int64_t status(int64_t device) {
+  const at::Device dev(at::kCUDA, static_cast<c10::DeviceIndex>(device));
+  c10::cuda::CUDAGuard guard(dev);
+  unsigned* word = status_word(dev);
+  unsigned host = 0;
+  cudaMemcpy(&host, word, sizeof(unsigned), cudaMemcpyDeviceToHost);
+  if (host != 0) cudaMemset(word, 0, sizeof(unsigned));
+  return static_cast<int64_t>(host);
+}
+
+std::tuple<int64_t, int64_t, int64_t> attention_plan(int64_t B, int64_t T, int64_t H, int64_t Hkv, int64_t S,
+                                                     int64_t sms) {
+  const ecz::AttnPlan p = ecz::attention_plan(B, T, H, Hkv, S, sms);
+  return {p.m_tiles, p.splits, p.chunks_per_split};
+}
+
+int64_t gemm_splits(int64_t M, int64_t N, int64_t K, int64_t sms) { return ecz::gemm_splits(M, N, K, sms); }
+
+}  // namespace
+
+PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
+  m.doc() = "economize_b200 sm_100a kernels (tcgen05 / TMA)";
+  m.def("rmsnorm", &rmsnorm, "fused residual add + RMSNorm");
+  m.def("rope_store", &rope_store, "rotary embedding + KV-cache write (+ optional QK-norm)");
+  m.def("attention", &attention, "tree-masked / causal attention over the slot cache (tcgen05)");
+  m.def("silu_mul", &silu_mul, "SwiGLU activation of [gate; up]");
+  m.def("linear", &linear, "x @ w.T on tcgen05 (swap-AB, split-K)");
+  m.def("argmax", &argmax, "row argmax");
+  m.def("greedy_accept", &greedy_accept, "longest accepted path of a verified draft tree");
+  m.def("kv_compact", &kv_compact, "move an accepted path's K/V to consecutive slots");
+  m.def("status", &status, "read and clear the device status word of bounded waits");
+  m.def("attention_plan", &attention_plan, "(m_tiles, splits, chunks_per_split) of an attention launch");
+  m.def("gemm_splits", &gemm_splits, "split-K factor of a GEMM launch");
+}

@@ -1,0 +1,351 @@
+// Memory-bound fused kernels of the decoder block and of the speculative-decoding cycle:
+//   * rmsnorm_kernel      fused residual add + RMSNorm (one CTA per token row, 16-byte vector loads)
+//   * rope_store_kernel   optional per-head RMSNorm (QK-norm families) + rotary embedding of q and k, and the
+//                         KV-cache write of k and v (one warp per token x head)
+//   * silu_mul_kernel     SwiGLU activation of a fused [gate; up] projection
+//   * argmax_kernel       first index of the row maximum (one CTA per row)
+//   * greedy_accept_kernel longest accepted path of a verified draft tree (one warp per row)
+//   * kv_compact_kernel   moves the accepted path's K/V to consecutive slots in all layers at once
+//
+// Rounding follows Hugging Face's Llama modules where it matters for greedy identity: the residual sum and the
+// normalized value are rounded to bf16 before the weight multiply, and the rotary products are rounded per term.
+#include "common.cuh"
+#include "launchers.h"
+
+namespace ecz {
+
+// ---------------------------------------------------------------------------------------------------------------
+// RMSNorm
+// ---------------------------------------------------------------------------------------------------------------
+template <int kMaxVec>
+__global__ void __launch_bounds__(256) rmsnorm_kernel(const bf16* __restrict__ x, const bf16* __restrict__ resid,
+                                                      const bf16* __restrict__ w, bf16* __restrict__ out,
+                                                      bf16* __restrict__ resid_out, int hidden, float eps) {
+  const int row = blockIdx.x;
+  const int nvec = hidden / 8;
+  const uint4* xv = reinterpret_cast<const uint4*>(x + static_cast<size_t>(row) * hidden);
+  const uint4* rv = resid ? reinterpret_cast<const uint4*>(resid + static_cast<size_t>(row) * hidden) : nullptr;
+  uint4* ro = reinterpret_cast<uint4*>(resid_out + static_cast<size_t>(row) * hidden);
+  float vals[kMaxVec][8];
+  float ss = 0.f;
+#pragma unroll
+  for (int i = 0; i < kMaxVec; ++i) {
+    const int v = threadIdx.x + i * blockDim.x;
+    if (v < nvec) {
+      uint4 a = xv[v];
+      const bf16* ap = reinterpret_cast<const bf16*>(&a);
+      uint4 s;
+      bf16* sp = reinterpret_cast<bf16*>(&s);
+      if (rv) {
+        uint4 b = rv[v];
+        const bf16* bp = reinterpret_cast<const bf16*>(&b);
+#pragma unroll
+        for (int j = 0; j < 8; ++j) sp[j] = __float2bfloat16(__bfloat162float(ap[j]) + __bfloat162float(bp[j]));
+      } else {
+        s = a;
+      }
+      ro[v] = s;
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        const float f = __bfloat162float(sp[j]);
+        vals[i][j] = f;
+        ss += f * f;
+      }
+    }
+  }
+  __shared__ float red[32];
+  ss = warp_sum(ss);
+  if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = ss;
+  __syncthreads();
+  if (threadIdx.x < 32) {
+    float t = threadIdx.x < (blockDim.x >> 5) ? red[threadIdx.x] : 0.f;
+    t = warp_sum(t);
+    if (threadIdx.x == 0) red[0] = t;
+  }
+  __syncthreads();
+  const float inv = rsqrtf(red[0] / static_cast<float>(hidden) + eps);
+  const uint4* wv = reinterpret_cast<const uint4*>(w);
+  uint4* ov = reinterpret_cast<uint4*>(out + static_cast<size_t>(row) * hidden);
+#pragma unroll
+  for (int i = 0; i < kMaxVec; ++i) {
+    const int v = threadIdx.x + i * blockDim.x;
+    if (v < nvec) {
+      uint4 ww = wv[v];
+      const bf16* wp = reinterpret_cast<const bf16*>(&ww);
+      uint4 o;
+      bf16* op = reinterpret_cast<bf16*>(&o);
+#pragma unroll
+      for (int j = 0; j < 8; ++j) op[j] = __float2bfloat16(__bfloat162float(wp[j]) * bf16r(vals[i][j] * inv));
+      ov[v] = o;
+    }
+  }
+}
+
+int launch_rmsnorm(const void* x, const void* resid, const void* w, void* out, void* resid_out, int rows, int hidden,
+                   float eps, cudaStream_t stream) {
+  if (hidden % 8 != 0 || hidden > 256 * 8 * 8) return -1;
+  const int nvec = hidden / 8;
+  int threads = nvec < 256 ? ((nvec + 31) / 32) * 32 : 256;
+  const int per = (nvec + threads - 1) / threads;
+  auto args = [&](auto kernel) {
+    kernel<<<rows, threads, 0, stream>>>(static_cast<const bf16*>(x), static_cast<const bf16*>(resid),
+                                         static_cast<const bf16*>(w), static_cast<bf16*>(out),
+                                         static_cast<bf16*>(resid_out), hidden, eps);
+  };
+  if (per <= 1) args(rmsnorm_kernel<1>);
+  else if (per <= 2) args(rmsnorm_kernel<2>);
+  else if (per <= 4) args(rmsnorm_kernel<4>);
+  else args(rmsnorm_kernel<8>);
+  return 0;
+}
+
+// ---------------------------------------------------------------------------------------------------------------
+// Rotary embedding + KV-cache store (+ optional per-head RMSNorm of q and k)
+// ---------------------------------------------------------------------------------------------------------------
+// qkv [B*T, (H + 2 Hkv) * D]; q_out [B*T, H, D]; caches [B, Hkv, S, D]; token (b, t) writes slot
+// kv_len[b] + q_offset + t when q_offset + t < n_new[b]. One warp per (token, head slot), head slot in
+// [0, H + Hkv): q heads first, then kv heads (k rotated and stored with its v).
+__global__ void __launch_bounds__(256) rope_store_kernel(
+    const bf16* __restrict__ qkv, const int* __restrict__ positions, const float* __restrict__ cos_t,
+    const float* __restrict__ sin_t, bf16* __restrict__ q_out, bf16* __restrict__ k_cache,
+    bf16* __restrict__ v_cache, const int* __restrict__ kv_len, const int* __restrict__ n_new,
+    const bf16* __restrict__ q_norm, const bf16* __restrict__ k_norm, float eps, int tokens, int T, int H, int Hkv,
+    int S, int q_offset) {
+  constexpr int D = 128;
+  const int warp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+  const int lane = threadIdx.x & 31;
+  const int slots = H + Hkv;
+  if (warp >= tokens * slots) return;
+  const int token = warp / slots;
+  const int head = warp % slots;
+  const int b = token / T, t = token % T;
+  const bool is_q = head < H;
+  const int width = (H + 2 * Hkv) * D;
+  const bf16* src = qkv + static_cast<size_t>(token) * width + (is_q ? head * D : H * D + (head - H) * D);
+  // lane owns elements (2*lane, 2*lane+1) of the first half and their partners in the second half
+  const int i0 = 2 * lane;
+  __nv_bfloat162 lo = *reinterpret_cast<const __nv_bfloat162*>(src + i0);
+  __nv_bfloat162 hi = *reinterpret_cast<const __nv_bfloat162*>(src + i0 + D / 2);
+  float x0 = __bfloat162float(lo.x), x1 = __bfloat162float(lo.y);
+  float y0 = __bfloat162float(hi.x), y1 = __bfloat162float(hi.y);
+  const bf16* nw = is_q ? q_norm : k_norm;
+  if (nw != nullptr) {
+    float ss = warp_sum(x0 * x0 + x1 * x1 + y0 * y0 + y1 * y1);
+    const float inv = rsqrtf(ss / D + eps);
+    x0 = __bfloat162float(nw[i0]) * bf16r(x0 * inv);
+    x1 = __bfloat162float(nw[i0 + 1]) * bf16r(x1 * inv);
+    y0 = __bfloat162float(nw[i0 + D / 2]) * bf16r(y0 * inv);
+    y1 = __bfloat162float(nw[i0 + D / 2 + 1]) * bf16r(y1 * inv);
+    x0 = bf16r(x0); x1 = bf16r(x1); y0 = bf16r(y0); y1 = bf16r(y1);
+  }
+  const int pos = positions[token];
+  const float* cp = cos_t + static_cast<size_t>(pos) * (D / 2) + i0;
+  const float* sp = sin_t + static_cast<size_t>(pos) * (D / 2) + i0;
+  const float c0 = bf16r(cp[0]), c1 = bf16r(cp[1]), s0 = bf16r(sp[0]), s1 = bf16r(sp[1]);
+  // out = x * cos + rotate_half(x) * sin, each product rounded to bf16 (HF computes it in the input dtype)
+  const float r0 = bf16r(bf16r(x0 * c0) + bf16r(-y0 * s0));
+  const float r1 = bf16r(bf16r(x1 * c1) + bf16r(-y1 * s1));
+  const float r2 = bf16r(bf16r(y0 * c0) + bf16r(x0 * s0));
+  const float r3 = bf16r(bf16r(y1 * c1) + bf16r(x1 * s1));
+  if (is_q) {
+    bf16* dst = q_out + (static_cast<size_t>(token) * H + head) * D;
+    *reinterpret_cast<__nv_bfloat162*>(dst + i0) = __floats2bfloat162_rn(r0, r1);
+    *reinterpret_cast<__nv_bfloat162*>(dst + i0 + D / 2) = __floats2bfloat162_rn(r2, r3);
+    return;
+  }
+  const int j = q_offset + t;
+  if (j >= n_new[b]) return;
+  const int kvh = head - H;
+  const size_t slot = static_cast<size_t>(kv_len[b]) + j;
+  const size_t off = ((static_cast<size_t>(b) * Hkv + kvh) * S + slot) * D;
+  *reinterpret_cast<__nv_bfloat162*>(k_cache + off + i0) = __floats2bfloat162_rn(r0, r1);
+  *reinterpret_cast<__nv_bfloat162*>(k_cache + off + i0 + D / 2) = __floats2bfloat162_rn(r2, r3);
+  const bf16* vsrc = qkv + static_cast<size_t>(token) * width + (H + Hkv) * D + kvh * D;
+  *reinterpret_cast<__nv_bfloat162*>(v_cache + off + i0) = *reinterpret_cast<const __nv_bfloat162*>(vsrc + i0);
+  *reinterpret_cast<__nv_bfloat162*>(v_cache + off + i0 + D / 2) =
+      *reinterpret_cast<const __nv_bfloat162*>(vsrc + i0 + D / 2);
+}
+
+int launch_rope_store(const void* qkv, const int* positions, const float* cos_t, const float* sin_t, void* q_out,
+                      void* k_cache, void* v_cache, const int* kv_len, const int* n_new, const void* q_norm,
+                      const void* k_norm, float eps, int B, int T, int H, int Hkv, int D, int S, int q_offset,
+                      cudaStream_t stream) {
+  if (D != 128) return -1;
+  const long warps = static_cast<long>(B) * T * (H + Hkv);
+  const int blocks = static_cast<int>((warps * 32 + 255) / 256);
+  rope_store_kernel<<<blocks, 256, 0, stream>>>(
+      static_cast<const bf16*>(qkv), positions, cos_t, sin_t, static_cast<bf16*>(q_out),
+      static_cast<bf16*>(k_cache), static_cast<bf16*>(v_cache), kv_len, n_new, static_cast<const bf16*>(q_norm),
+      static_cast<const bf16*>(k_norm), eps, B * T, T, H, Hkv, S, q_offset);
+  return 0;
+}
+
+// ---------------------------------------------------------------------------------------------------------------
+// SiLU(gate) * up
+// ---------------------------------------------------------------------------------------------------------------
+__global__ void __launch_bounds__(256) silu_mul_kernel(const bf16* __restrict__ gu, bf16* __restrict__ out,
+                                                       int rows, int F) {
+  const long total = static_cast<long>(rows) * (F / 8);
+  for (long i = blockIdx.x * static_cast<long>(blockDim.x) + threadIdx.x; i < total;
+       i += static_cast<long>(gridDim.x) * blockDim.x) {
+    const long r = i / (F / 8), c = i % (F / 8);
+    const uint4 g = reinterpret_cast<const uint4*>(gu + r * 2 * F)[c];
+    const uint4 u = reinterpret_cast<const uint4*>(gu + r * 2 * F + F)[c];
+    const bf16* gp = reinterpret_cast<const bf16*>(&g);
+    const bf16* up = reinterpret_cast<const bf16*>(&u);
+    uint4 o;
+    bf16* op = reinterpret_cast<bf16*>(&o);
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      const float x = __bfloat162float(gp[j]);
+      const float s = bf16r(x / (1.f + expf(-x)));
+      op[j] = __float2bfloat16(s * __bfloat162float(up[j]));
+    }
+    reinterpret_cast<uint4*>(out + r * F)[c] = o;
+  }
+}
+
+int launch_silu_mul(const void* gu, void* out, int rows, int F, cudaStream_t stream) {
+  if (F % 8 != 0) return -1;
+  const long total = static_cast<long>(rows) * (F / 8);
+  int blocks = static_cast<int>(std::min<long>((total + 255) / 256, 148L * 16));
+  if (blocks < 1) blocks = 1;
+  silu_mul_kernel<<<blocks, 256, 0, stream>>>(static_cast<const bf16*>(gu), static_cast<bf16*>(out), rows, F);
+  return 0;
+}
+
+// ---------------------------------------------------------------------------------------------------------------
+// Row argmax (first maximal index), bf16 or fp32 input
+// ---------------------------------------------------------------------------------------------------------------
+template <typename T>
+__device__ __forceinline__ float to_f(T v);
+template <>
+__device__ __forceinline__ float to_f<bf16>(bf16 v) { return __bfloat162float(v); }
+template <>
+__device__ __forceinline__ float to_f<float>(float v) { return v; }
+
+template <typename T>
+__global__ void __launch_bounds__(512) argmax_kernel(const T* __restrict__ x, int64_t* __restrict__ out, int V) {
+  const T* row = x + static_cast<size_t>(blockIdx.x) * V;
+  float best = -INFINITY;
+  int idx = 0x7fffffff;
+  for (int i = threadIdx.x; i < V; i += blockDim.x) {
+    const float v = to_f<T>(row[i]);
+    if (v > best) { best = v; idx = i; }  // strided scan: the first hit per thread is its smallest index
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+    const float ob = __shfl_xor_sync(0xffffffffu, best, o);
+    const int oi = __shfl_xor_sync(0xffffffffu, idx, o);
+    if (ob > best || (ob == best && oi < idx)) { best = ob; idx = oi; }
+  }
+  __shared__ float sb[16];
+  __shared__ int si[16];
+  if ((threadIdx.x & 31) == 0) { sb[threadIdx.x >> 5] = best; si[threadIdx.x >> 5] = idx; }
+  __syncthreads();
+  if (threadIdx.x < 32) {
+    const int nw = blockDim.x >> 5;
+    best = threadIdx.x < nw ? sb[threadIdx.x] : -INFINITY;
+    idx = threadIdx.x < nw ? si[threadIdx.x] : 0x7fffffff;
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+      const float ob = __shfl_xor_sync(0xffffffffu, best, o);
+      const int oi = __shfl_xor_sync(0xffffffffu, idx, o);
+      if (ob > best || (ob == best && oi < idx)) { best = ob; idx = oi; }
+    }
+    if (threadIdx.x == 0) out[blockIdx.x] = idx == 0x7fffffff ? 0 : idx;
+  }
+}
+
+int launch_argmax(const void* x, bool is_bf16, int64_t* out, int rows, int V, cudaStream_t stream) {
+  if (rows == 0) return 0;
+  if (is_bf16) argmax_kernel<bf16><<<rows, 512, 0, stream>>>(static_cast<const bf16*>(x), out, V);
+  else argmax_kernel<float><<<rows, 512, 0, stream>>>(static_cast<const float*>(x), out, V);
+  return 0;
+}
+
+// ---------------------------------------------------------------------------------------------------------------
+// Greedy acceptance of a draft tree (chains are trees with parent t-1)
+// ---------------------------------------------------------------------------------------------------------------
+// One warp per row; T <= 64 nodes. Node t (t >= 1) is accepted when its parent is and tokens[t] == pred[parent].
+// The deepest accepted node (first on ties) ends the path. Outputs n_acc [B], path [B, T] (node of the i-th path
+// position, padded with the last node) and out [B, T] (path tokens after the root, then the bonus pred[last]).
+__global__ void greedy_accept_kernel(const int64_t* __restrict__ tokens, const int64_t* __restrict__ parents,
+                                     const int64_t* __restrict__ pred, int* __restrict__ n_acc,
+                                     int* __restrict__ path, int64_t* __restrict__ out, int T) {
+  const int b = blockIdx.x;
+  const int lane = threadIdx.x;
+  __shared__ int acc[64], depth[64], par[64];
+  const int64_t* tk = tokens + static_cast<size_t>(b) * T;
+  const int64_t* pa = parents + static_cast<size_t>(b) * T;
+  const int64_t* pr = pred + static_cast<size_t>(b) * T;
+  for (int t = lane; t < T; t += 32) par[t] = t == 0 ? -1 : static_cast<int>(pa[t]);
+  __syncwarp();
+  if (lane == 0) {
+    acc[0] = 1;
+    depth[0] = 0;
+    int best = 0, best_depth = 0;
+    for (int t = 1; t < T; ++t) {
+      const int p = par[t];
+      const bool ok = p >= 0 && p < t && acc[p] && tk[t] == pr[p];
+      acc[t] = ok;
+      depth[t] = (p >= 0 && p < t) ? depth[p] + 1 : 0;
+      if (ok && depth[t] > best_depth) { best_depth = depth[t]; best = t; }
+    }
+    n_acc[b] = best_depth;
+    int node = best;
+    for (int i = best_depth; i >= 0; --i) {  // walk up from the last node
+      path[static_cast<size_t>(b) * T + i] = node;
+      if (i >= 1) out[static_cast<size_t>(b) * T + i - 1] = tk[node];
+      node = i > 0 ? par[node] : 0;
+    }
+    for (int i = best_depth + 1; i < T; ++i) path[static_cast<size_t>(b) * T + i] = best;
+    out[static_cast<size_t>(b) * T + best_depth] = pr[best];
+    for (int i = best_depth + 1; i < T; ++i) out[static_cast<size_t>(b) * T + i] = 0;
+  }
+}
+
+int launch_greedy_accept(const int64_t* tokens, const int64_t* parents, const int64_t* pred, int* n_acc, int* path,
+                         int64_t* out, int B, int T, cudaStream_t stream) {
+  if (T > 64) return -1;
+  greedy_accept_kernel<<<B, 32, 0, stream>>>(tokens, parents, pred, n_acc, path, out, T);
+  return 0;
+}
+
+// ---------------------------------------------------------------------------------------------------------------
+// KV compaction after a tree pass: cache [L*2, B, Hkv, S, D]; slot kv_len + path[i] -> kv_len + i, i <= n_acc.
+// One CTA per (layer*2 + kv, b, kv head); every thread reads its 16-byte chunk first, then all write, so
+// overlapping source/destination slots of one path never race.
+// ---------------------------------------------------------------------------------------------------------------
+__global__ void kv_compact_kernel(bf16* __restrict__ cache, const int* __restrict__ kv_len,
+                                  const int* __restrict__ path, const int* __restrict__ n_acc, int B, int Hkv, int S,
+                                  int D, int T) {
+  const int lh = blockIdx.x;  // layer*2 + kv
+  const int b = blockIdx.y, h = blockIdx.z;
+  const int n = n_acc[b];
+  const int vecs = D / 8;
+  const int i = threadIdx.x / vecs + 1;  // path position (the root at 0 never moves)
+  const int c = threadIdx.x % vecs;
+  bf16* base = cache + ((static_cast<size_t>(lh) * B + b) * Hkv + h) * static_cast<size_t>(S) * D;
+  const int start = kv_len[b];
+  uint4 v = make_uint4(0, 0, 0, 0);
+  const bool active = i <= n && i < T;
+  int src = 0;
+  if (active) {
+    src = path[static_cast<size_t>(b) * T + i];
+    v = reinterpret_cast<const uint4*>(base + static_cast<size_t>(start + src) * D)[c];
+  }
+  __syncthreads();
+  if (active && src != i) reinterpret_cast<uint4*>(base + static_cast<size_t>(start + i) * D)[c] = v;
+}
+
+int launch_kv_compact(void* cache, const int* kv_len, const int* path, const int* n_acc, int LH, int B, int Hkv,
+                      int S, int D, int T, int max_depth, cudaStream_t stream) {
+  const int threads = max_depth * (D / 8);
+  if (threads > 1024 || D % 8) return -1;
+  dim3 grid(LH, B, Hkv);
+  kv_compact_kernel<<<grid, threads, 0, stream>>>(static_cast<bf16*>(cache), kv_len, path, n_acc, B, Hkv, S, D, T);
+  return 0;
+}
+
+}  // namespace ecz

@@ -1,0 +1,219 @@
+// tcgen05 / TMA GEMM for the decoder's projections: Y[M, N] = X[M, K] . W[N, K]^T (bf16 in, fp32 accumulate).
+//
+// Decode passes have few token rows (a verified draft tree is ~61 rows per sequence) and large weights, so the
+// kernel swaps the operands: the UMMA "A" operand is a 128-row tile of W (128 output features on the 128 TMEM
+// lanes) and the "B" operand a BN-row tile of X (tokens on the UMMA N side, BN in {32, 64, 128, 256}). The
+// accumulator D[n, m] lives in TMEM (BN fp32 columns); the epilogue reads it with tcgen05.ld and writes Y[m, n].
+//
+// Pipeline: one elected TMA thread streams (W, X) K-slices of 64 elements (128-byte swizzled rows) into a ring of
+// `STAGES` shared-memory stages guarded by full/empty mbarriers; one elected MMA thread issues 4 UMMAs (K = 16
+// each) per stage and releases the stage with tcgen05.commit; the accumulator barrier wakes the epilogue.
+//
+// When the tile grid cannot fill the 148 SMs, K is split over `splits` CTAs per tile, each writing fp32 partials
+// to a workspace that a second kernel sums (and rounds to bf16). Every wait is bounded (common.cuh).
+#include <algorithm>
+
+#include "common.cuh"
+#include "launchers.h"
+
+namespace ecz {
+
+namespace {
+
+constexpr int kBM = 128;  // W rows per tile (UMMA M)
+constexpr int kBK = 64;   // K elements per stage (one 128-byte swizzle row)
+constexpr int kABytes = kBM * kBK * 2;
+
+template <int BN>
+struct GemmCfg {
+  static constexpr int kBBytes = BN * kBK * 2;
+  static constexpr int kStageBytes = kABytes + kBBytes;
+  static constexpr int kStages = std::min(8, (200 * 1024) / kStageBytes);
+  static constexpr int kTmemCols = BN < 32 ? 32 : BN;
+  static constexpr int kSmem = kStages * kStageBytes + 1024 /*align*/ + 256 /*barriers*/;
+};
+
+template <int BN>
+__global__ void __launch_bounds__(128, 1)
+    gemm_swapab_kernel(const __grid_constant__ CUtensorMap tm_w, const __grid_constant__ CUtensorMap tm_x,
+                       bf16* __restrict__ y, float* __restrict__ ws, int M, int N, int K, int kb_per_split,
+                       unsigned* status) {
+  using Cfg = GemmCfg<BN>;
+  constexpr int S = Cfg::kStages;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* a_tiles = smem;
+  uint8_t* b_tiles = smem + S * kABytes;
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + S * Cfg::kStageBytes);
+  uint64_t* empty = full + S;
+  uint64_t* accum = empty + S;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(accum + 1);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int n0 = blockIdx.x * kBM, m0 = blockIdx.y * BN, split = blockIdx.z;
+  const int total_kb = (K + kBK - 1) / kBK;
+  const int kb0 = split * kb_per_split;
+  const int nkb = std::min(kb_per_split, total_kb - kb0);
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < S; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1);
+    }
+    mbar_init(accum, 1);
+    *abort_flag = 0;
+    fence_mbar_init();
+    tma_prefetch_desc(&tm_w);
+    tma_prefetch_desc(&tm_x);
+  }
+  __syncwarp();
+  if (warp == 0) tmem_alloc(tmem_slot, Cfg::kTmemCols);
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+
+  if (nkb > 0 && warp == 0 && lane == 0) {
+    // ---- TMA producer ----
+    for (int kb = 0; kb < nkb; ++kb) {
+      const int s = kb % S;
+      const uint32_t use = kb / S;
+      if (kb >= S && !mbar_wait(&empty[s], (use & 1u) ^ 1u, status, kStatusWaitEmpty, abort_flag)) break;
+      mbar_arrive_expect_tx(&full[s], Cfg::kStageBytes);
+      const int kx = (kb0 + kb) * kBK;
+      tma_load_2d(a_tiles + s * kABytes, &tm_w, &full[s], kx, n0);
+      tma_load_2d(b_tiles + s * Cfg::kBBytes, &tm_x, &full[s], kx, m0);
+    }
+  } else if (nkb > 0 && warp == 1 && lane == 0) {
+    // ---- MMA issuer ----
+    constexpr uint32_t idesc = idesc_bf16_f32(kBM, BN);
+    for (int kb = 0; kb < nkb; ++kb) {
+      const int s = kb % S;
+      const uint32_t use = kb / S;
+      if (!mbar_wait(&full[s], use & 1u, status, kStatusWaitFull, abort_flag)) break;
+      tc_fence_after();
+      const uint32_t a_addr = smem_u32(a_tiles + s * kABytes);
+      const uint32_t b_addr = smem_u32(b_tiles + s * Cfg::kBBytes);
+#pragma unroll
+      for (int kk = 0; kk < kBK / 16; ++kk) {
+        umma_bf16(tmem, desc_kmajor_sw128(a_addr + kk * 32), desc_kmajor_sw128(b_addr + kk * 32), idesc,
+                  (kb | kk) != 0 ? 1u : 0u);
+      }
+      umma_commit(&empty[s]);
+    }
+    umma_commit(accum);  // also on abort, so the epilogue's wait ends
+  }
+  __syncwarp();
+
+  // ---- epilogue: warp w owns TMEM lanes 32w..32w+31 = output features n0 + 32w + lane ----
+  if (nkb > 0) mbar_wait(accum, 0, status, kStatusWaitAccum, abort_flag);
+  __syncthreads();  // a failed wait set abort_flag; the decision below is uniform across the CTA
+  tc_fence_after();
+  const bool ok = nkb > 0 && !*abort_flag;
+  const int n = n0 + warp * 32 + lane;
+  if (ok) {
+    const uint32_t lane_base = tmem + (static_cast<uint32_t>(warp * 32) << 16);
+#pragma unroll 1
+    for (int c = 0; c < BN; c += 16) {
+      float v[16];
+      tmem_ld16(lane_base + c, v);
+      if (n < N) {
+        if (ws == nullptr) {
+#pragma unroll
+          for (int j = 0; j < 16; ++j) {
+            const int m = m0 + c + j;
+            if (m < M) y[static_cast<size_t>(m) * N + n] = __float2bfloat16(v[j]);
+          }
+        } else {
+          float* part = ws + static_cast<size_t>(split) * M * N;
+#pragma unroll
+          for (int j = 0; j < 16; ++j) {
+            const int m = m0 + c + j;
+            if (m < M) part[static_cast<size_t>(m) * N + n] = v[j];
+          }
+        }
+      }
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 0) tmem_dealloc(tmem, Cfg::kTmemCols);
+}
+
+__global__ void __launch_bounds__(256) splitk_reduce_kernel(const float* __restrict__ ws, bf16* __restrict__ y,
+                                                             long total, int splits) {
+  for (long i = (blockIdx.x * static_cast<long>(blockDim.x) + threadIdx.x) * 4; i < total;
+       i += static_cast<long>(gridDim.x) * blockDim.x * 4) {
+    float4 acc = *reinterpret_cast<const float4*>(ws + i);
+    for (int s = 1; s < splits; ++s) {
+      const float4 p = *reinterpret_cast<const float4*>(ws + static_cast<size_t>(s) * total + i);
+      acc.x += p.x; acc.y += p.y; acc.z += p.z; acc.w += p.w;
+    }
+    __nv_bfloat162 lo = __floats2bfloat162_rn(acc.x, acc.y);
+    __nv_bfloat162 hi = __floats2bfloat162_rn(acc.z, acc.w);
+    uint2 packed;
+    packed.x = *reinterpret_cast<uint32_t*>(&lo);
+    packed.y = *reinterpret_cast<uint32_t*>(&hi);
+    *reinterpret_cast<uint2*>(y + i) = packed;
+  }
+}
+
+template <int BN>
+int run_gemm(const CUtensorMap& tm_w, const CUtensorMap& tm_x, void* y, float* ws, int M, int N, int K,
+             int splits, unsigned* status, cudaStream_t stream) {
+  using Cfg = GemmCfg<BN>;
+  static bool configured = false;
+  if (!configured) {
+    cudaFuncSetAttribute(gemm_swapab_kernel<BN>, cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg::kSmem);
+    configured = true;
+  }
+  const int total_kb = (K + kBK - 1) / kBK;
+  const int kbps = (total_kb + splits - 1) / splits;
+  splits = (total_kb + kbps - 1) / kbps;  // no empty split
+  dim3 grid((N + kBM - 1) / kBM, (M + BN - 1) / BN, splits);
+  gemm_swapab_kernel<BN><<<grid, 128, Cfg::kSmem, stream>>>(tm_w, tm_x, static_cast<bf16*>(y),
+                                                            splits > 1 ? ws : nullptr, M, N, K, kbps, status);
+  if (splits > 1) {
+    const long total = static_cast<long>(M) * N;
+    const int blocks = static_cast<int>(std::min<long>((total / 4 + 255) / 256, 148L * 8));
+    splitk_reduce_kernel<<<std::max(blocks, 1), 256, 0, stream>>>(ws, static_cast<bf16*>(y), total, splits);
+  }
+  return 0;
+}
+
+}  // namespace
+
+int gemm_block_n(int M) {
+  if (M <= 32) return 32;
+  if (M <= 64) return 64;
+  if (M <= 128) return 128;
+  return 256;
+}
+
+// Split count from the weight shape (and, for large M, the token tiles): enough CTAs to cover the SMs, at least
+// 4 K-slices per split. Depends on M only through the number of token tiles, so every decode pass of up to
+// 256 rows reduces each output in the same order.
+int gemm_splits(int M, int N, int K, int num_sms) {
+  const int bn = gemm_block_n(M);
+  const int m_tiles = (M + bn - 1) / bn;
+  const int tiles = ((N + kBM - 1) / kBM) * m_tiles;
+  const int total_kb = (K + kBK - 1) / kBK;
+  if (tiles >= num_sms) return 1;
+  int splits = num_sms / tiles;
+  splits = std::min(splits, total_kb / 4);
+  return std::max(1, std::min(splits, 16));
+}
+
+int launch_gemm_bf16(const CUtensorMap* tm_w, const CUtensorMap* tm_x, void* y, float* ws, int M, int N, int K,
+                     int splits, unsigned* status, cudaStream_t stream) {
+  if (K % 8 != 0 || N % 4 != 0) return -1;
+  switch (gemm_block_n(M)) {
+    case 32: return run_gemm<32>(*tm_w, *tm_x, y, ws, M, N, K, splits, status, stream);
+    case 64: return run_gemm<64>(*tm_w, *tm_x, y, ws, M, N, K, splits, status, stream);
+    case 128: return run_gemm<128>(*tm_w, *tm_x, y, ws, M, N, K, splits, status, stream);
+    default: return run_gemm<256>(*tm_w, *tm_x, y, ws, M, N, K, splits, status, stream);
+  }
+}
+
+}  // namespace ecz

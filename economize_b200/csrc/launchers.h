@@ -1,0 +1,48 @@
+// Host-side entry points of the CUDA kernels (raw pointers; the torch bindings check shapes and dtypes).
+#pragma once
+
+#include <cuda.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+namespace ecz {
+
+struct AttnPlan {
+  int m_tiles = 1;
+  int splits = 1;
+  int chunks_per_split = 1;
+  long ws_floats = 0;
+};
+
+// elementwise.cu
+int launch_rmsnorm(const void* x, const void* resid, const void* w, void* out, void* resid_out, int rows, int hidden,
+                   float eps, cudaStream_t stream);
+int launch_rope_store(const void* qkv, const int* positions, const float* cos_t, const float* sin_t, void* q_out,
+                      void* k_cache, void* v_cache, const int* kv_len, const int* n_new, const void* q_norm,
+                      const void* k_norm, float eps, int B, int T, int H, int Hkv, int D, int S, int q_offset,
+                      cudaStream_t stream);
+int launch_silu_mul(const void* gu, void* out, int rows, int F, cudaStream_t stream);
+int launch_argmax(const void* x, bool is_bf16, int64_t* out, int rows, int V, cudaStream_t stream);
+int launch_greedy_accept(const int64_t* tokens, const int64_t* parents, const int64_t* pred, int* n_acc, int* path,
+                         int64_t* out, int B, int T, cudaStream_t stream);
+int launch_kv_compact(void* cache, const int* kv_len, const int* path, const int* n_acc, int LH, int B, int Hkv,
+                      int S, int D, int T, int max_depth, cudaStream_t stream);
+
+// gemm_tc.cu
+int gemm_block_n(int M);
+int gemm_splits(int M, int N, int K, int num_sms);
+int launch_gemm_bf16(const CUtensorMap* tm_w, const CUtensorMap* tm_x, void* y, float* ws, int M, int N, int K,
+                     int splits, unsigned* status, cudaStream_t stream);
+
+// attention.cu
+AttnPlan attention_plan(int B, int T, int H, int Hkv, int S, int num_sms);
+int launch_attention(const void* q, const CUtensorMap* tm_k, const CUtensorMap* tm_v, void* out, float* ws,
+                     const int* kv_len, const int* n_new, const int64_t* mask, int B, int T, int H, int Hkv, int D,
+                     int S, float scale, int q_offset, const AttnPlan& plan, unsigned* status, cudaStream_t stream);
+
+// tmap.cpp: a 2-D bf16 tensor map over a row-major [rows, cols] matrix with a {64, box_rows} box and the 128-byte
+// swizzle (cols * 2 bytes must be a multiple of 16). Returns 0 on success.
+int make_tmap_2d_bf16(CUtensorMap* map, const void* base, uint64_t rows, uint64_t cols, uint64_t row_stride_elems,
+                      uint32_t box_rows);
+
+}  // namespace ecz

@@ -1,0 +1,191 @@
+"""Architecture description of the decoder models the engine executes.
+
+:class:`ModelConfig` is read from a Hugging Face ``config.json`` / ``PretrainedConfig`` (the families economize's
+``arch/families/llama.py``, ``mistral.py``, ``qwen2.py``, ``qwen3.py`` and ``mixtral.py`` adapters cover) or built
+directly, e.g. :func:`llama31_8b` for the benchmark's random-init Llama-3.1-8B architecture.
+"""
+
+from __future__ import annotations
+
+import math
+from dataclasses import asdict, dataclass, field
+from typing import Any
+
+import torch
+
+from ..errors import UnsupportedModelError
+
+__all__ = ["ModelConfig", "SUPPORTED_MODEL_TYPES", "llama31_8b", "llama31_70b", "mixtral_8x7b", "rope_inv_freq",
+           "tiny_llama"]
+
+#: ``model_type`` values whose decoder layer is the Llama block (pre-norm attention + gated MLP), with the
+#: differences expressed as fields: q/k/v bias (qwen2), per-head q/k RMSNorm (qwen3), sparse MoE MLP (mixtral).
+SUPPORTED_MODEL_TYPES = ("llama", "mistral", "qwen2", "qwen3", "mixtral", "economize_b200")
+
+
+@dataclass
+class ModelConfig:
+    vocab_size: int
+    hidden_size: int
+    intermediate_size: int
+    num_layers: int
+    num_heads: int
+    num_kv_heads: int
+    head_dim: int | None = None
+    rms_norm_eps: float = 1e-5
+    rope_theta: float = 10000.0
+    rope_scaling: dict[str, Any] | None = None
+    max_position_embeddings: int = 8192
+    tie_word_embeddings: bool = False
+    attention_bias: bool = False
+    qk_norm: bool = False
+    num_experts: int = 0
+    experts_per_token: int = 2
+    model_type: str = "llama"
+    extra: dict[str, Any] = field(default_factory=dict)
+
+    def __post_init__(self) -> None:
+        if self.head_dim is None:
+            self.head_dim = self.hidden_size // self.num_heads
+        if self.num_heads % self.num_kv_heads:
+            raise UnsupportedModelError(f"{self.num_heads} heads do not split into {self.num_kv_heads} KV groups")
+
+    @property
+    def q_size(self) -> int:
+        return self.num_heads * self.head_dim
+
+    @property
+    def kv_size(self) -> int:
+        return self.num_kv_heads * self.head_dim
+
+    @property
+    def is_moe(self) -> bool:
+        return self.num_experts > 0
+
+    def num_parameters(self) -> int:
+        h, f, layers = self.hidden_size, self.intermediate_size, self.num_layers
+        attn = h * (self.q_size + 2 * self.kv_size) + self.q_size * h
+        mlp = 3 * h * f * (self.num_experts if self.is_moe else 1) + (h * self.num_experts if self.is_moe else 0)
+        embed = self.vocab_size * h * (1 if self.tie_word_embeddings else 2)
+        return layers * (attn + mlp + 2 * h) + embed + h
+
+    def to_dict(self) -> dict[str, Any]:
+        return asdict(self)
+
+    @classmethod
+    def from_dict(cls, data: dict[str, Any]) -> ModelConfig:
+        known = set(cls.__dataclass_fields__)
+        return cls(**{k: v for k, v in data.items() if k in known})
+
+    @classmethod
+    def from_hf(cls, hf: Any) -> ModelConfig:
+        """From a ``transformers`` config object or its ``config.json`` dict."""
+        get = (lambda k, d=None: hf.get(k, d)) if isinstance(hf, dict) else (lambda k, d=None: getattr(hf, k, d))
+        model_type = get("model_type", "llama")
+        if model_type not in SUPPORTED_MODEL_TYPES:
+            raise UnsupportedModelError(f"model_type {model_type!r} is not supported; supported: "
+                                        f"{', '.join(SUPPORTED_MODEL_TYPES)}")
+        rope = get("rope_scaling") or get("rope_parameters")
+        theta = get("rope_theta")
+        if theta is None and isinstance(rope, dict):
+            theta = rope.get("rope_theta")
+        if isinstance(rope, dict) and rope.get("rope_type", rope.get("type", "default")) in ("default", None):
+            rope = None
+        heads = int(get("num_attention_heads"))
+        return cls(
+            vocab_size=int(get("vocab_size")),
+            hidden_size=int(get("hidden_size")),
+            intermediate_size=int(get("intermediate_size")),
+            num_layers=int(get("num_hidden_layers")),
+            num_heads=heads,
+            num_kv_heads=int(get("num_key_value_heads") or heads),
+            head_dim=get("head_dim"),
+            rms_norm_eps=float(get("rms_norm_eps", 1e-6)),
+            rope_theta=float(theta if theta is not None else 10000.0),
+            rope_scaling=dict(rope) if isinstance(rope, dict) else None,
+            max_position_embeddings=int(get("max_position_embeddings", 8192)),
+            tie_word_embeddings=bool(get("tie_word_embeddings", False)),
+            attention_bias=bool(get("attention_bias", model_type == "qwen2")),
+            qk_norm=model_type == "qwen3",
+            num_experts=int(get("num_local_experts", 0) or 0),
+            experts_per_token=int(get("num_experts_per_tok", 2) or 2),
+            model_type=model_type,
+        )
+
+    def to_hf(self) -> Any:
+        """A ``transformers`` config of the same architecture (for the HF oracle and the reference benchmark)."""
+        import transformers
+
+        common = dict(vocab_size=self.vocab_size, hidden_size=self.hidden_size,
+                      intermediate_size=self.intermediate_size, num_hidden_layers=self.num_layers,
+                      num_attention_heads=self.num_heads, num_key_value_heads=self.num_kv_heads,
+                      head_dim=self.head_dim, rms_norm_eps=self.rms_norm_eps, rope_theta=self.rope_theta,
+                      max_position_embeddings=self.max_position_embeddings,
+                      tie_word_embeddings=self.tie_word_embeddings, attention_bias=self.attention_bias)
+        if self.rope_scaling is not None:
+            common["rope_scaling"] = dict(self.rope_scaling)
+        if self.is_moe:
+            return transformers.MixtralConfig(num_local_experts=self.num_experts,
+                                              num_experts_per_tok=self.experts_per_token,
+                                              **{k: v for k, v in common.items() if k != "attention_bias"})
+        return transformers.LlamaConfig(**common)
+
+
+def rope_inv_freq(config: ModelConfig) -> torch.Tensor:
+    """Inverse frequencies ``[D/2]`` (fp32) of the rotary embedding, with Llama-3 frequency scaling when
+    ``rope_scaling`` says so (the published Llama 3.1 rule: long wavelengths divided by ``factor``, short ones
+    kept, a linear blend of the two in between)."""
+    dim = config.head_dim
+    inv = 1.0 / (config.rope_theta ** (torch.arange(0, dim, 2, dtype=torch.int64).float() / dim))
+    scaling = config.rope_scaling or {}
+    kind = scaling.get("rope_type", scaling.get("type"))
+    if kind == "llama3":
+        factor = float(scaling["factor"])
+        low, high = float(scaling.get("low_freq_factor", 1.0)), float(scaling.get("high_freq_factor", 4.0))
+        original = float(scaling.get("original_max_position_embeddings", 8192))
+        low_wavelen, high_wavelen = original / low, original / high
+        wavelen = 2 * math.pi / inv
+        scaled = torch.where(wavelen > low_wavelen, inv / factor, inv)
+        smooth = (original / wavelen - low) / (high - low)
+        blended = (1 - smooth) * scaled / factor + smooth * scaled
+        medium = ~(wavelen < high_wavelen) & ~(wavelen > low_wavelen)
+        inv = torch.where(medium, blended, scaled)
+    elif kind == "linear":
+        inv = inv / float(scaling["factor"])
+    elif kind not in (None, "default"):
+        raise UnsupportedModelError(f"rope_scaling type {kind!r} is not supported")
+    return inv
+
+
+def llama31_8b(**overrides: Any) -> ModelConfig:
+    """Llama-3.1-8B architecture (32 layers, hidden 4096, 32/8 heads, FFN 14336, vocab 128256)."""
+    cfg = dict(vocab_size=128256, hidden_size=4096, intermediate_size=14336, num_layers=32, num_heads=32,
+               num_kv_heads=8, head_dim=128, rms_norm_eps=1e-5, rope_theta=500000.0,
+               rope_scaling={"rope_type": "llama3", "factor": 8.0, "low_freq_factor": 1.0,
+                             "high_freq_factor": 4.0, "original_max_position_embeddings": 8192},
+               max_position_embeddings=131072)
+    cfg.update(overrides)
+    return ModelConfig(**cfg)
+
+
+def llama31_70b(**overrides: Any) -> ModelConfig:
+    """Llama-3.1-70B architecture (80 layers, hidden 8192, 64/8 heads, FFN 28672)."""
+    return llama31_8b(**{"hidden_size": 8192, "intermediate_size": 28672, "num_layers": 80, "num_heads": 64,
+                         **overrides})
+
+
+def mixtral_8x7b(**overrides: Any) -> ModelConfig:
+    """Mixtral-8x7B architecture (32 layers, hidden 4096, 8 experts top-2, expert FFN 14336)."""
+    cfg = dict(vocab_size=32000, hidden_size=4096, intermediate_size=14336, num_layers=32, num_heads=32,
+               num_kv_heads=8, head_dim=128, rms_norm_eps=1e-5, rope_theta=1e6, max_position_embeddings=32768,
+               num_experts=8, experts_per_token=2, model_type="mixtral")
+    cfg.update(overrides)
+    return ModelConfig(**cfg)
+
+
+def tiny_llama(**overrides: Any) -> ModelConfig:
+    """The CPU plumbing configuration: 4 layers, hidden 256, 4 heads / 2 KV heads, FFN 688, vocab 1024, θ=1e4."""
+    cfg = dict(vocab_size=1024, hidden_size=256, intermediate_size=688, num_layers=4, num_heads=4, num_kv_heads=2,
+               rms_norm_eps=1e-6, rope_theta=1e4, max_position_embeddings=2048)
+    cfg.update(overrides)
+    return ModelConfig(**cfg)

@@ -1,0 +1,93 @@
+"""Conversion between Hugging Face state dicts and the engine's fused parameter layout.
+
+Names follow ``transformers`` 5 (``model.layers.{i}.self_attn.q_proj.weight`` ..., Mixtral experts as fused
+``mlp.experts.gate_up_proj [E, 2F, H]`` / ``down_proj [E, H, F]``; the older per-expert ``block_sparse_moe.experts.
+{e}.w1/w2/w3`` layout is read too).
+"""
+
+from __future__ import annotations
+
+import torch
+
+from ..errors import CheckpointFormatError
+
+__all__ = ["export_hf_state", "load_hf_state"]
+
+
+def _take(state: dict[str, torch.Tensor], key: str) -> torch.Tensor:
+    if key not in state:
+        raise CheckpointFormatError(f"missing weight {key!r}")
+    return state[key]
+
+
+@torch.no_grad()
+def load_hf_state(model, state: dict[str, torch.Tensor]) -> None:
+    """Copy a Hugging Face state dict into ``model`` (a :class:`~economize_b200.models.CausalLM`)."""
+    c = model.config
+    model.embed.copy_(_take(state, "model.embed_tokens.weight"))
+    model.norm.copy_(_take(state, "model.norm.weight"))
+    if model.lm_head is not None:
+        model.lm_head.copy_(state.get("lm_head.weight", state["model.embed_tokens.weight"]))
+    for i, layer in enumerate(model.layers):
+        p = f"model.layers.{i}."
+        a = p + "self_attn."
+        layer.wqkv.copy_(torch.cat([_take(state, a + f"{n}_proj.weight") for n in "qkv"], 0))
+        if layer.bqkv is not None:
+            layer.bqkv.copy_(torch.cat([_take(state, a + f"{n}_proj.bias") for n in "qkv"], 0))
+        layer.wo.copy_(_take(state, a + "o_proj.weight"))
+        if layer.q_norm is not None:
+            layer.q_norm.copy_(_take(state, a + "q_norm.weight"))
+            layer.k_norm.copy_(_take(state, a + "k_norm.weight"))
+        layer.attn_norm.copy_(_take(state, p + "input_layernorm.weight"))
+        layer.mlp_norm.copy_(_take(state, p + "post_attention_layernorm.weight"))
+        if c.is_moe:
+            if p + "mlp.experts.gate_up_proj" in state:
+                layer.router.copy_(_take(state, p + "mlp.gate.weight"))
+                layer.w_gate_up.copy_(state[p + "mlp.experts.gate_up_proj"])
+                layer.w_down.copy_(_take(state, p + "mlp.experts.down_proj"))
+            else:
+                m = p + "block_sparse_moe."
+                layer.router.copy_(_take(state, m + "gate.weight"))
+                for e in range(c.num_experts):
+                    x = m + f"experts.{e}."
+                    layer.w_gate_up[e].copy_(torch.cat([_take(state, x + "w1.weight"),
+                                                        _take(state, x + "w3.weight")], 0))
+                    layer.w_down[e].copy_(_take(state, x + "w2.weight"))
+        else:
+            m = p + "mlp."
+            layer.w_gate_up.copy_(torch.cat([_take(state, m + "gate_proj.weight"),
+                                             _take(state, m + "up_proj.weight")], 0))
+            layer.w_down.copy_(_take(state, m + "down_proj.weight"))
+
+
+@torch.no_grad()
+def export_hf_state(model) -> dict[str, torch.Tensor]:
+    """The Hugging Face state dict of ``model`` (split projections, ``transformers`` 5 names)."""
+    c = model.config
+    out = {"model.embed_tokens.weight": model.embed.detach().clone(), "model.norm.weight": model.norm.detach().clone()}
+    if model.lm_head is not None:
+        out["lm_head.weight"] = model.lm_head.detach().clone()
+    for i, layer in enumerate(model.layers):
+        p = f"model.layers.{i}."
+        q, k, v = layer.wqkv.detach().split([c.q_size, c.kv_size, c.kv_size], 0)
+        for n, w in zip("qkv", (q, k, v)):
+            out[p + f"self_attn.{n}_proj.weight"] = w.clone()
+        if layer.bqkv is not None:
+            for n, w in zip("qkv", layer.bqkv.detach().split([c.q_size, c.kv_size, c.kv_size], 0)):
+                out[p + f"self_attn.{n}_proj.bias"] = w.clone()
+        out[p + "self_attn.o_proj.weight"] = layer.wo.detach().clone()
+        if layer.q_norm is not None:
+            out[p + "self_attn.q_norm.weight"] = layer.q_norm.detach().clone()
+            out[p + "self_attn.k_norm.weight"] = layer.k_norm.detach().clone()
+        out[p + "input_layernorm.weight"] = layer.attn_norm.detach().clone()
+        out[p + "post_attention_layernorm.weight"] = layer.mlp_norm.detach().clone()
+        if c.is_moe:
+            out[p + "mlp.gate.weight"] = layer.router.detach().clone()
+            out[p + "mlp.experts.gate_up_proj"] = layer.w_gate_up.detach().clone()
+            out[p + "mlp.experts.down_proj"] = layer.w_down.detach().clone()
+        else:
+            g, u = layer.w_gate_up.detach().chunk(2, 0)
+            out[p + "mlp.gate_proj.weight"] = g.clone()
+            out[p + "mlp.up_proj.weight"] = u.clone()
+            out[p + "mlp.down_proj.weight"] = layer.w_down.detach().clone()
+    return out

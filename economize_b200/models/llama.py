@@ -1,0 +1,192 @@
+"""The engine's own decoder executor for Llama-family models (Llama, Mistral, Qwen2, Qwen3, and Mixtral-style MoE).
+
+Weights are stored fused for the GEMM kernels: ``wqkv = [W_q; W_k; W_v]`` and ``w_gate_up = [W_gate; W_up]`` (one
+read of the activations per projection group), in contrast to economize, which calls the Hugging Face decoder layers
+(``src/economize/arch/base.py:406-414``). A forward pass runs every layer through :mod:`economize_b200.ops`:
+
+    x, r = rmsnorm(h, attn_norm, r)          # fused residual add + RMSNorm (r: output of the previous blocks)
+    q    = rope_store(x @ wqkv.T, cache)      # fused rotary embedding + KV-cache write
+    h    = attention(q, cache) @ wo.T         # tree / causal attention over the slot cache
+    x, r = rmsnorm(h, mlp_norm, r)
+    h    = silu_mul(x @ w_gate_up.T) @ w_down.T
+
+Block outputs that a drafter reads (EAGLE-3's low/mid/high features) are the residual stream ``r`` at the start of
+the following block, so capturing them costs nothing.
+"""
+
+from __future__ import annotations
+
+from typing import Any
+
+import torch
+from torch import nn
+
+from .. import ops
+from ..runtime.cache import KVCache, StepBatch
+from .config import ModelConfig, rope_inv_freq
+
+__all__ = ["CausalLM", "DecoderLayer", "init_weights"]
+
+
+class DecoderLayer(nn.Module):
+    """Parameters of one pre-norm decoder block (dense or sparse-MoE MLP)."""
+
+    def __init__(self, config: ModelConfig, dtype: torch.dtype, device: torch.device | str | None) -> None:
+        super().__init__()
+        h, f = config.hidden_size, config.intermediate_size
+        kw = dict(dtype=dtype, device=device)
+        self.attn_norm = nn.Parameter(torch.ones(h, **kw))
+        self.wqkv = nn.Parameter(torch.empty(config.q_size + 2 * config.kv_size, h, **kw))
+        self.bqkv = nn.Parameter(torch.zeros(config.q_size + 2 * config.kv_size, **kw)) if config.attention_bias \
+            else None
+        self.wo = nn.Parameter(torch.empty(h, config.q_size, **kw))
+        self.q_norm = nn.Parameter(torch.ones(config.head_dim, **kw)) if config.qk_norm else None
+        self.k_norm = nn.Parameter(torch.ones(config.head_dim, **kw)) if config.qk_norm else None
+        self.mlp_norm = nn.Parameter(torch.ones(h, **kw))
+        if config.is_moe:
+            e = config.num_experts
+            self.router = nn.Parameter(torch.empty(e, h, **kw))
+            self.w_gate_up = nn.Parameter(torch.empty(e, 2 * f, h, **kw))
+            self.w_down = nn.Parameter(torch.empty(e, h, f, **kw))
+        else:
+            self.router = None
+            self.w_gate_up = nn.Parameter(torch.empty(2 * f, h, **kw))
+            self.w_down = nn.Parameter(torch.empty(h, f, **kw))
+
+
+class CausalLM(nn.Module):
+    """A decoder-only language model executed by the engine's kernels.
+
+    Args:
+        config: The architecture.
+        dtype: Parameter and activation dtype (bf16 on the GPU, fp32 for the CPU oracle).
+        device: Where the parameters live.
+    """
+
+    def __init__(self, config: ModelConfig, dtype: torch.dtype = torch.bfloat16,
+                 device: torch.device | str | None = None) -> None:
+        super().__init__()
+        self.config = config
+        kw = dict(dtype=dtype, device=device)
+        self.embed = nn.Parameter(torch.empty(config.vocab_size, config.hidden_size, **kw))
+        self.layers = nn.ModuleList(DecoderLayer(config, dtype, device) for _ in range(config.num_layers))
+        self.norm = nn.Parameter(torch.ones(config.hidden_size, **kw))
+        self.lm_head = None if config.tie_word_embeddings else nn.Parameter(
+            torch.empty(config.vocab_size, config.hidden_size, **kw))
+        self._rope: tuple[torch.Tensor, torch.Tensor] | None = None
+
+    # ---- properties --------------------------------------------------------------------------------------------
+    @property
+    def device(self) -> torch.device:
+        return self.embed.device
+
+    @property
+    def dtype(self) -> torch.dtype:
+        return self.embed.dtype
+
+    @property
+    def head_weight(self) -> torch.Tensor:
+        return self.embed if self.lm_head is None else self.lm_head
+
+    def rope_tables(self, length: int | None = None) -> tuple[torch.Tensor, torch.Tensor]:
+        """``cos, sin [P, D/2]`` fp32 for positions ``0..P-1`` (computed once per device, like HF: the angle is the
+        fp32 product of the position and the inverse frequency)."""
+        need = max(length or 0, self.config.max_position_embeddings)
+        if self._rope is None or self._rope[0].shape[0] < need or self._rope[0].device != self.device:
+            inv = rope_inv_freq(self.config).to(self.device)
+            pos = torch.arange(need, device=self.device, dtype=torch.float32)
+            angles = pos[:, None] * inv[None, :]
+            self._rope = (angles.cos().contiguous(), angles.sin().contiguous())
+        return self._rope
+
+    def new_cache(self, batch: int, capacity: int) -> KVCache:
+        c = self.config
+        return KVCache(c.num_layers, batch, c.num_kv_heads, capacity, c.head_dim, self.dtype, self.device)
+
+    # ---- forward -----------------------------------------------------------------------------------------------
+    def embed_tokens(self, tokens: torch.Tensor) -> torch.Tensor:
+        return self.embed[tokens]
+
+    def forward_step(self, tokens: torch.Tensor, batch: StepBatch, cache: KVCache,
+                     capture: tuple[int, ...] = (), layers: range | None = None,
+                     ) -> tuple[torch.Tensor, dict[int, torch.Tensor]]:
+        """Run a pass over ``tokens [B, T]``; returns the final-normed hidden states ``[B, T, H]`` and the captured
+        block outputs ``{i: [B, T, H]}`` (``0``: the embeddings, ``i``: the output of ``i`` blocks)."""
+        c = self.config
+        cos, sin = self.rope_tables()
+        h = self.embed_tokens(tokens)
+        resid: torch.Tensor | None = None
+        aux: dict[int, torch.Tensor] = {}
+        todo = layers if layers is not None else range(c.num_layers)
+        for i in todo:
+            layer = self.layers[i]
+            x, resid = ops.rmsnorm(h, layer.attn_norm, c.rms_norm_eps, resid)
+            if i in capture:
+                aux[i] = resid
+            h = self._attention(layer, i, x, batch, cache, cos, sin)
+            x, resid = ops.rmsnorm(h, layer.mlp_norm, c.rms_norm_eps, resid)
+            h = self._mlp(layer, x)
+        out, resid = ops.rmsnorm(h, self.norm, c.rms_norm_eps, resid)
+        if c.num_layers in capture:
+            aux[c.num_layers] = resid
+        return out, aux
+
+    def _attention(self, layer: DecoderLayer, index: int, x: torch.Tensor, batch: StepBatch, cache: KVCache,
+                   cos: torch.Tensor, sin: torch.Tensor) -> torch.Tensor:
+        c = self.config
+        qkv = ops.linear(x, layer.wqkv, layer.bqkv)
+        k_cache, v_cache = cache.layer(index)
+        q = ops.rope_store(qkv, batch.positions, cos, sin, c.num_heads, c.num_kv_heads, c.head_dim, k_cache,
+                           v_cache, batch.kv_len, batch.n_new, layer.q_norm, layer.k_norm, c.rms_norm_eps,
+                           q_offset=batch.q_offset)
+        o = ops.attention(q, k_cache, v_cache, batch.kv_len, batch.n_new, batch.mask, q_offset=batch.q_offset)
+        return ops.linear(o.reshape(*o.shape[:2], -1), layer.wo)
+
+    def _mlp(self, layer: DecoderLayer, x: torch.Tensor) -> torch.Tensor:
+        if layer.router is not None:
+            from ..parallel.moe import moe_mlp
+
+            return moe_mlp(x, layer.router, layer.w_gate_up, layer.w_down, self.config.experts_per_token)
+        return ops.linear(ops.silu_mul(ops.linear(x, layer.w_gate_up)), layer.w_down)
+
+    def logits(self, hidden: torch.Tensor) -> torch.Tensor:
+        return ops.linear(hidden, self.head_weight)
+
+    # ---- Hugging Face interop ----------------------------------------------------------------------------------
+    @classmethod
+    def from_hf(cls, hf_model: nn.Module, dtype: torch.dtype | None = None,
+                device: torch.device | str | None = None) -> CausalLM:
+        """Build from a ``transformers`` causal LM of a supported family (weights are copied into fused tensors)."""
+        from .hf import load_hf_state
+
+        config = ModelConfig.from_hf(hf_model.config)
+        first = next(hf_model.parameters())
+        model = cls(config, dtype or first.dtype, device or first.device)
+        load_hf_state(model, hf_model.state_dict())
+        return model
+
+    def hf_state_dict(self) -> dict[str, torch.Tensor]:
+        from .hf import export_hf_state
+
+        return export_hf_state(self)
+
+
+@torch.no_grad()
+def init_weights(model: CausalLM, seed: int = 0, std: float = 0.02) -> CausalLM:
+    """Random initialisation N(0, std) of every matrix (norms at one), generated on the model's device from
+    ``seed`` in a fixed order, so two processes build identical weights."""
+    gen = torch.Generator(device=model.device)
+    gen.manual_seed(seed)
+    for name, p in model.named_parameters():
+        if p.dim() >= 2:
+            p.copy_(torch.randn(p.shape, generator=gen, device=p.device, dtype=torch.float32).mul_(std))
+        elif "norm" in name:
+            p.fill_(1.0)
+        else:
+            p.zero_()
+    return model
+
+
+def describe(model: CausalLM) -> dict[str, Any]:
+    c = model.config
+    return {"layers": c.num_layers, "hidden": c.hidden_size, "params": c.num_parameters(), "dtype": str(model.dtype)}

@@ -1,0 +1,98 @@
+"""Operators of the decode engine.
+
+Every operator takes the hand-written sm_100a kernel of ``economize_b200._C`` for CUDA tensors and the PyTorch
+implementation of :mod:`.reference` for CPU tensors. There is no third path: a CUDA tensor with the extension
+missing raises :class:`~economize_b200.errors.KernelUnavailableError`.
+"""
+
+from __future__ import annotations
+
+import torch
+
+from . import reference
+from ._ext import available, load_error, require
+
+__all__ = [
+    "argmax",
+    "attention",
+    "available",
+    "greedy_accept",
+    "kv_compact",
+    "linear",
+    "load_error",
+    "require",
+    "rmsnorm",
+    "rope_store",
+    "silu_mul",
+]
+
+
+def rmsnorm(x: torch.Tensor, weight: torch.Tensor, eps: float,
+            residual: torch.Tensor | None = None) -> tuple[torch.Tensor, torch.Tensor]:
+    """Fused residual add + RMSNorm: ``(norm(x + residual) * weight, x + residual)`` over the last dim."""
+    if x.is_cuda:
+        return require().rmsnorm(x, weight, float(eps), residual)
+    return reference.rmsnorm(x, weight, eps, residual)
+
+
+def rope_store(qkv: torch.Tensor, positions: torch.Tensor, cos: torch.Tensor, sin: torch.Tensor, num_heads: int,
+               num_kv_heads: int, head_dim: int, k_cache: torch.Tensor, v_cache: torch.Tensor,
+               kv_len: torch.Tensor, n_new: torch.Tensor, q_norm: torch.Tensor | None = None,
+               k_norm: torch.Tensor | None = None, eps: float = 1e-6, q_offset: int = 0) -> torch.Tensor:
+    """Fused (per-head RMSNorm +) rotary embedding of queries and keys and the KV-cache write (see
+    :func:`.reference.rope_store`)."""
+    if qkv.is_cuda:
+        return require().rope_store(qkv, positions, cos, sin, num_heads, num_kv_heads, head_dim, k_cache, v_cache,
+                                    kv_len, n_new, q_norm, k_norm, float(eps), int(q_offset))
+    return reference.rope_store(qkv, positions, cos, sin, num_heads, num_kv_heads, head_dim, k_cache, v_cache,
+                                kv_len, n_new, q_norm, k_norm, eps, q_offset)
+
+
+def attention(q: torch.Tensor, k_cache: torch.Tensor, v_cache: torch.Tensor, kv_len: torch.Tensor,
+              n_new: torch.Tensor, mask: torch.Tensor | None = None, scale: float | None = None,
+              q_offset: int = 0) -> torch.Tensor:
+    """Causal / tree-masked attention over the slot cache (see :func:`.reference.attention`)."""
+    scale = float(scale if scale is not None else q.shape[-1] ** -0.5)
+    if q.is_cuda:
+        return require().attention(q, k_cache, v_cache, kv_len, n_new, mask, scale, int(q_offset))
+    return reference.attention(q, k_cache, v_cache, kv_len, n_new, mask, scale, q_offset=q_offset)
+
+
+def silu_mul(gate_up: torch.Tensor) -> torch.Tensor:
+    if gate_up.is_cuda:
+        return require().silu_mul(gate_up)
+    return reference.silu_mul(gate_up)
+
+
+def linear(x: torch.Tensor, weight: torch.Tensor, bias: torch.Tensor | None = None) -> torch.Tensor:
+    """``x @ weight.T (+ bias)``; on CUDA the tcgen05/TMA GEMM of ``csrc/gemm_tc.cu``."""
+    if x.is_cuda:
+        shape = x.shape
+        y = require().linear(x.reshape(-1, shape[-1]), weight)
+        y = y.reshape(*shape[:-1], weight.shape[0])
+        return y if bias is None else y + bias
+    return reference.linear(x, weight, bias)
+
+
+def argmax(x: torch.Tensor) -> torch.Tensor:
+    """Index of the largest entry of every row of ``x [..., V]`` (first one on ties), as int64."""
+    if x.is_cuda:
+        shape = x.shape
+        return require().argmax(x.reshape(-1, shape[-1])).reshape(shape[:-1])
+    return x.argmax(-1)
+
+
+def greedy_accept(tokens: torch.Tensor, parents: torch.Tensor, pred: torch.Tensor
+                  ) -> tuple[torch.Tensor, torch.Tensor, torch.Tensor]:
+    """Longest accepted path of a greedily verified chain or tree (see :func:`.reference.greedy_accept`)."""
+    if tokens.is_cuda:
+        return require().greedy_accept(tokens, parents, pred)
+    return reference.greedy_accept(tokens, parents, pred)
+
+
+def kv_compact(cache: torch.Tensor, kv_len: torch.Tensor, path: torch.Tensor, n_acc: torch.Tensor) -> None:
+    """Move an accepted path's cache entries to consecutive slots in every layer (in place)."""
+    if cache.is_cuda:
+        require().kv_compact(cache, kv_len, path, n_acc)
+        return
+    reference.kv_compact(cache, kv_len, path, n_acc)

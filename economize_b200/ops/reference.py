@@ -1,0 +1,184 @@
+"""Plain PyTorch implementations of every operator (CPU path and fp32 numerics oracle of the CUDA kernels).
+
+Each function computes the same thing as the kernel of the same name in ``economize_b200/csrc``. The dtype
+behaviour follows Hugging Face's Llama modules where the result is rounded (RMSNorm rounds the normalized value to
+the input dtype before the weight multiply; rotary products are taken in the input dtype), so fp32 runs on CPU
+reproduce ``transformers`` exactly.
+"""
+
+from __future__ import annotations
+
+import torch
+import torch.nn.functional as F
+
+__all__ = [
+    "attention",
+    "greedy_accept",
+    "kv_compact",
+    "linear",
+    "rmsnorm",
+    "rope_store",
+    "silu_mul",
+    "visible_mask",
+]
+
+
+def rmsnorm(x: torch.Tensor, weight: torch.Tensor, eps: float,
+            residual: torch.Tensor | None = None) -> tuple[torch.Tensor, torch.Tensor]:
+    """``(norm(x + residual) * weight, x + residual)``; the sum is rounded to ``x.dtype`` first."""
+    summed = x if residual is None else (x + residual)
+    h = summed.float()
+    h = h * torch.rsqrt(h.pow(2).mean(-1, keepdim=True) + eps)
+    return weight * h.to(x.dtype), summed
+
+
+def _rotate(x: torch.Tensor, cos: torch.Tensor, sin: torch.Tensor) -> torch.Tensor:
+    half = x.shape[-1] // 2
+    rot = torch.cat((-x[..., half:], x[..., :half]), -1)
+    c = torch.cat((cos, cos), -1).to(x.dtype)
+    s = torch.cat((sin, sin), -1).to(x.dtype)
+    return x * c + rot * s
+
+
+def rope_store(qkv: torch.Tensor, positions: torch.Tensor, cos: torch.Tensor, sin: torch.Tensor, num_heads: int,
+               num_kv_heads: int, head_dim: int, k_cache: torch.Tensor, v_cache: torch.Tensor,
+               kv_len: torch.Tensor, n_new: torch.Tensor, q_norm: torch.Tensor | None = None,
+               k_norm: torch.Tensor | None = None, eps: float = 1e-6, q_offset: int = 0) -> torch.Tensor:
+    """Rotate queries and keys of ``qkv [B, T, (H + 2 H_kv) D]`` (optionally after a per-head RMSNorm), write the keys
+    and values of token ``t`` to cache slot ``kv_len[b] + q_offset + t`` of ``k_cache/v_cache [B, H_kv, S, D]`` when
+    ``q_offset + t < n_new[b]``, and return the rotated queries ``[B, T, H, D]``."""
+    batch, length, _ = qkv.shape
+    q, k, v = qkv.split([num_heads * head_dim, num_kv_heads * head_dim, num_kv_heads * head_dim], -1)
+    q = q.reshape(batch, length, num_heads, head_dim)
+    k = k.reshape(batch, length, num_kv_heads, head_dim)
+    v = v.reshape(batch, length, num_kv_heads, head_dim)
+    if q_norm is not None:
+        q = rmsnorm(q, q_norm, eps)[0]
+    if k_norm is not None:
+        k = rmsnorm(k, k_norm, eps)[0]
+    pos = positions.long()
+    c, s = cos[pos][:, :, None], sin[pos][:, :, None]  # [B, T, 1, D/2]
+    q, k = _rotate(q, c, s), _rotate(k, c, s)
+    for b in range(batch):
+        n, start = min(int(n_new[b]) - q_offset, length), int(kv_len[b]) + q_offset
+        if n > 0:
+            k_cache[b, :, start:start + n] = k[b, :n].transpose(0, 1).to(k_cache.dtype)
+            v_cache[b, :, start:start + n] = v[b, :n].transpose(0, 1).to(v_cache.dtype)
+    return q
+
+
+def visible_mask(kv_len: torch.Tensor, n_new: torch.Tensor, length: int, width: int,
+                 mask: torch.Tensor | None, q_offset: int = 0) -> torch.Tensor:
+    """Boolean ``[B, T, width]`` visibility of cache slots for the queries of a pass (see :func:`attention`)."""
+    device = kv_len.device
+    slots = torch.arange(width, device=device)
+    t = torch.arange(length, device=device)
+    base = kv_len.long()[:, None, None]
+    prefix = slots[None, None, :] < base  # [B, 1, W]
+    j = slots[None, None, :] - base  # index of the new token in that slot
+    valid_new = (j >= 0) & (j < n_new.long()[:, None, None])
+    if mask is None:
+        new_vis = j <= (q_offset + t)[None, :, None]
+    else:
+        bits = mask.long()[:, :, None]  # [B, T, 1]
+        jj = j.clamp(0, 63)
+        new_vis = ((bits >> jj) & 1).bool()
+    return prefix | (valid_new & new_vis)
+
+
+def attention(q: torch.Tensor, k_cache: torch.Tensor, v_cache: torch.Tensor, kv_len: torch.Tensor,
+              n_new: torch.Tensor, mask: torch.Tensor | None = None, scale: float | None = None,
+              softcap: float | None = None, q_offset: int = 0) -> torch.Tensor:
+    """Attention of queries ``[B, T, H, D]`` over the slot cache ``[B, H_kv, S, D]``.
+
+    Query ``t`` of row ``b`` sees every committed slot ``< kv_len[b]`` and the new tokens' slots ``kv_len[b] + j``
+    (``j < n_new[b]``) for which bit ``j`` of ``mask[b, t]`` is set (``mask=None``: causal, ``j <= q_offset + t``).
+    Heads are grouped: query head ``h`` reads KV head ``h // (H / H_kv)``.
+    """
+    batch, length, heads, dim = q.shape
+    kv_heads = k_cache.shape[1]
+    width = max(int((kv_len + n_new).max()), 1)
+    vis = visible_mask(kv_len, n_new, length, width, mask, q_offset)  # [B, T, W]
+    keys = k_cache[:, :, :width].float()
+    values = v_cache[:, :, :width].float()
+    group = heads // kv_heads
+    keys = keys.repeat_interleave(group, 1)
+    values = values.repeat_interleave(group, 1)
+    scores = torch.matmul(q.float().transpose(1, 2), keys.transpose(-1, -2)) * (scale or dim ** -0.5)
+    if softcap is not None:
+        scores = torch.tanh(scores / softcap) * softcap
+    scores = scores.masked_fill(~vis[:, None], float("-inf"))
+    probs = torch.softmax(scores, -1).nan_to_num(0.0)
+    out = torch.matmul(probs, values).transpose(1, 2)
+    return out.to(q.dtype)
+
+
+def silu_mul(gate_up: torch.Tensor) -> torch.Tensor:
+    """``silu(gate) * up`` for ``gate_up = [..., 2F]`` holding the gate first (rounded like HF's Llama MLP)."""
+    gate, up = gate_up.chunk(2, -1)
+    return F.silu(gate) * up
+
+
+def linear(x: torch.Tensor, weight: torch.Tensor, bias: torch.Tensor | None = None) -> torch.Tensor:
+    return F.linear(x, weight, bias)
+
+
+def greedy_accept(tokens: torch.Tensor, parents: torch.Tensor, pred: torch.Tensor
+                  ) -> tuple[torch.Tensor, torch.Tensor, torch.Tensor]:
+    """Longest accepted path of a verified draft tree.
+
+    Args:
+        tokens: ``[B, T]`` tokens of the pass: node 0 is the root (the last committed token), nodes ``1..T-1`` the
+            drafts in topological order.
+        parents: ``[B, T]`` parent node of every node (``parents[:, 0]`` is ignored); a chain has ``parents[t] = t-1``.
+        pred: ``[B, T]`` the exact model's choice after every node.
+
+    Returns:
+        ``n_acc [B]`` accepted drafts, ``path [B, T]`` node index of the path's ``i``-th node (``path[:, 0] = 0``,
+        entries past ``n_acc`` repeat the last node), and ``out [B, T]`` the tokens the cycle commits after the root:
+        the path's draft tokens followed by the bonus token ``pred[last node]``.
+    """
+    batch, length = tokens.shape
+    device = tokens.device
+    acc = torch.zeros(batch, length, dtype=torch.bool, device=device)
+    depth = torch.zeros(batch, length, dtype=torch.long, device=device)
+    acc[:, 0] = True
+    for t in range(1, length):
+        p = parents[:, t].long().clamp_min(0)
+        par_acc = acc.gather(1, p[:, None])[:, 0]
+        ok = par_acc & (tokens[:, t] == pred.gather(1, p[:, None])[:, 0]) & (parents[:, t] >= 0)
+        acc[:, t] = ok
+        depth[:, t] = depth.gather(1, p[:, None])[:, 0] + 1
+    score = torch.where(acc, depth, torch.full_like(depth, -1))
+    # deepest accepted node, first one on ties
+    best_depth = score.max(1).values
+    idx = torch.arange(length, device=device)[None].expand(batch, length)
+    best = torch.where(score == best_depth[:, None], idx, torch.full_like(idx, length)).min(1).values
+    n_acc = best_depth
+    path = torch.zeros(batch, length, dtype=torch.long, device=device)
+    out = torch.zeros(batch, length, dtype=tokens.dtype, device=device)
+    for b in range(batch):
+        node, chain = int(best[b]), []
+        while node > 0:
+            chain.append(node)
+            node = int(parents[b, node])
+        chain = chain[::-1]
+        nodes = [0, *chain]
+        for i, n in enumerate(nodes):
+            path[b, i] = n
+        for i in range(len(nodes), length):
+            path[b, i] = nodes[-1]
+        for i, n in enumerate(chain):
+            out[b, i] = tokens[b, n]
+        out[b, len(chain)] = pred[b, nodes[-1]]
+    return n_acc.to(torch.int32), path.to(torch.int32), out
+
+
+def kv_compact(cache: torch.Tensor, kv_len: torch.Tensor, path: torch.Tensor, n_acc: torch.Tensor) -> None:
+    """Move the cache entries of an accepted tree path to consecutive slots: slot ``kv_len + path[b, i]`` to
+    ``kv_len + i`` for ``i <= n_acc[b]``, in every layer of ``cache [L, 2, B, H_kv, S, D]``."""
+    for b in range(cache.shape[2]):
+        n, base = int(n_acc[b]), int(kv_len[b])
+        src = base + path[b, : n + 1].long()
+        moved = cache[:, :, b, :, src].clone()
+        cache[:, :, b, :, base:base + n + 1] = moved

@@ -1,0 +1,183 @@
+"""Numerics of every CUDA kernel against the plain PyTorch fp32 implementation of the same op
+(economize_b200.ops.reference), at small shapes that cover the tile edges (tile-unaligned M, N, K, slots), GQA
+packing, tree masks, causal prefill with ragged rows, and split-K / split-key reductions."""
+
+import pytest
+import torch
+
+from economize_b200 import ops
+from economize_b200.ops import reference as ref
+
+pytestmark = pytest.mark.gpu
+
+
+def _close(a, b, atol, rtol=2e-2):
+    torch.testing.assert_close(a.float(), b.float(), atol=atol, rtol=rtol)
+
+
+@pytest.mark.parametrize("rows,hidden", [(1, 4096), (61, 4096), (7, 256), (33, 8192)])
+@pytest.mark.parametrize("with_resid", [False, True])
+def test_rmsnorm(cuda, rows, hidden, with_resid):
+    g = torch.Generator(device=cuda).manual_seed(0)
+    x = torch.randn(rows, hidden, device=cuda, generator=g).bfloat16()
+    r = torch.randn(rows, hidden, device=cuda, generator=g).bfloat16() if with_resid else None
+    w = (1 + 0.1 * torch.randn(hidden, device=cuda, generator=g)).bfloat16()
+    out, res = ops.rmsnorm(x, w, 1e-5, r)
+    e_out, e_res = ref.rmsnorm(x, w, 1e-5, r)  # same bf16 rounding steps, computed by torch
+    _close(res, e_res, 0, 0)
+    _close(out, e_out, 2e-2)
+    exact = ref.rmsnorm(x.float(), w.float(), 1e-5, None if r is None else r.float())[0]
+    _close(out, exact, 5e-2)
+
+
+@pytest.mark.parametrize("M,N,K", [(1, 256, 256), (61, 6144, 4096), (64, 512, 688), (200, 1024, 512),
+                                   (300, 384, 1024), (5, 128256 // 16, 4096)])
+def test_linear(cuda, M, N, K):
+    g = torch.Generator(device=cuda).manual_seed(1)
+    x = torch.randn(M, K, device=cuda, generator=g).bfloat16()
+    w = (torch.randn(N, K, device=cuda, generator=g) * 0.02).bfloat16()
+    y = ops.linear(x, w)
+    expect = x.float() @ w.float().T
+    _close(y, expect, 2e-2 * expect.abs().max().item() / 4 + 1e-3)
+    assert ops.require().status(0) == 0
+
+
+def test_linear_deterministic_in_rows(cuda):
+    """A row's result does not depend on how many other rows the launch has (up to 256 rows)."""
+    g = torch.Generator(device=cuda).manual_seed(2)
+    x = torch.randn(61, 4096, device=cuda, generator=g).bfloat16()
+    w = (torch.randn(4096, 4096, device=cuda, generator=g) * 0.02).bfloat16()
+    full = ops.linear(x, w)
+    one = ops.linear(x[:1].contiguous(), w)
+    assert torch.equal(full[:1], one) or (full[:1] - one).abs().max().item() < 1e-2
+
+
+def _cache(B, Hkv, S, D, dev, g):
+    k = (torch.randn(B, Hkv, S, D, device=dev, generator=g)).bfloat16()
+    v = (torch.randn(B, Hkv, S, D, device=dev, generator=g)).bfloat16()
+    return k, v
+
+
+def _tree_mask(B, T, dev, g):
+    """Random topological trees: node 0 the root, every node's parent an earlier node; bits = ancestors + self."""
+    masks = torch.zeros(B, T, dtype=torch.int64)
+    for b in range(B):
+        anc = [1]
+        for t in range(1, T):
+            p = int(torch.randint(0, t, (1,)))
+            anc.append(anc[p] | (1 << t))
+        masks[b] = torch.tensor([a if a < 2**63 else a - 2**64 for a in anc])
+    return masks.to(dev)
+
+
+@pytest.mark.parametrize("B,T,H,Hkv,S,lens", [
+    (1, 61, 32, 8, 832, [512]),      # the benchmark's tree pass
+    (2, 61, 8, 2, 300, [120, 37]),   # ragged, slots not a multiple of the key tile
+    (3, 1, 32, 8, 700, [600, 1, 129]),  # plain decode
+    (2, 10, 4, 4, 200, [0, 64]),     # no GQA
+])
+def test_tree_attention(cuda, B, T, H, Hkv, S, lens):
+    g = torch.Generator(device=cuda).manual_seed(3)
+    D = 128
+    k, v = _cache(B, Hkv, S, D, cuda, g)
+    q = torch.randn(B, T, H, D, device=cuda, generator=g).bfloat16()
+    kv_len = torch.tensor(lens, dtype=torch.int32, device=cuda)
+    n_new = torch.full((B,), T, dtype=torch.int32, device=cuda)
+    mask = _tree_mask(B, T, cuda, g)
+    out = ops.attention(q, k, v, kv_len, n_new, mask)
+    expect = ref.attention(q.float(), k.float(), v.float(), kv_len, n_new, mask)
+    _close(out, expect, 2e-2)
+    assert ops.require().status(0) == 0
+
+
+@pytest.mark.parametrize("B,T,H,Hkv,lens", [(1, 512, 32, 8, [512]), (3, 200, 8, 2, [200, 17, 150]),
+                                            (2, 40, 4, 2, [40, 39])])
+def test_causal_prefill_attention(cuda, B, T, H, Hkv, lens):
+    g = torch.Generator(device=cuda).manual_seed(4)
+    D, S = 128, T + 64
+    k, v = _cache(B, Hkv, S, D, cuda, g)
+    q = torch.randn(B, T, H, D, device=cuda, generator=g).bfloat16()
+    kv_len = torch.zeros(B, dtype=torch.int32, device=cuda)
+    n_new = torch.tensor(lens, dtype=torch.int32, device=cuda)
+    out = ops.attention(q, k, v, kv_len, n_new, None)
+    expect = ref.attention(q.float(), k.float(), v.float(), kv_len, n_new, None)
+    for b, n in enumerate(lens):
+        _close(out[b, :n], expect[b, :n], 2e-2)
+
+
+def test_attention_q_offset(cuda):
+    """A drafter's tree step: queries are the last W nodes of a forwarded region, visible by ancestor bits."""
+    g = torch.Generator(device=cuda).manual_seed(5)
+    B, W, H, Hkv, S, D = 2, 10, 8, 2, 256, 128
+    k, v = _cache(B, Hkv, S, D, cuda, g)
+    q = torch.randn(B, W, H, D, device=cuda, generator=g).bfloat16()
+    kv_len = torch.tensor([100, 7], dtype=torch.int32, device=cuda)
+    n_new = torch.full((B,), 30, dtype=torch.int32, device=cuda)
+    full = _tree_mask(B, 30, cuda, g)
+    mask = full[:, 20:].contiguous()
+    out = ops.attention(q, k, v, kv_len, n_new, mask, q_offset=20)
+    expect = ref.attention(q.float(), k.float(), v.float(), kv_len, n_new, mask, q_offset=20)
+    _close(out, expect, 2e-2)
+
+
+@pytest.mark.parametrize("qk_norm", [False, True])
+def test_rope_store(cuda, qk_norm):
+    g = torch.Generator(device=cuda).manual_seed(6)
+    B, T, H, Hkv, D, S = 2, 7, 8, 2, 128, 64
+    qkv = torch.randn(B, T, (H + 2 * Hkv) * D, device=cuda, generator=g).bfloat16()
+    pos = torch.randint(0, 40, (B, T), device=cuda, generator=g, dtype=torch.int32)
+    inv = 1.0 / (10000 ** (torch.arange(0, D, 2, device=cuda).float() / D))
+    ang = torch.arange(64, device=cuda).float()[:, None] * inv[None]
+    cos, sin = ang.cos().contiguous(), ang.sin().contiguous()
+    kv_len = torch.tensor([3, 20], dtype=torch.int32, device=cuda)
+    n_new = torch.tensor([7, 5], dtype=torch.int32, device=cuda)
+    qn = (1 + 0.1 * torch.randn(D, device=cuda, generator=g)).bfloat16() if qk_norm else None
+    kn = (1 + 0.1 * torch.randn(D, device=cuda, generator=g)).bfloat16() if qk_norm else None
+    kc, vc = torch.zeros(B, Hkv, S, D, device=cuda).bfloat16(), torch.zeros(B, Hkv, S, D, device=cuda).bfloat16()
+    kr, vr = kc.clone(), vc.clone()
+    q = ops.rope_store(qkv, pos, cos, sin, H, Hkv, D, kc, vc, kv_len, n_new, qn, kn, 1e-6)
+    qe = ref.rope_store(qkv, pos, cos, sin, H, Hkv, D, kr, vr, kv_len, n_new, qn, kn, 1e-6)
+    _close(q, qe, 2e-2)
+    _close(kc, kr, 2e-2)
+    _close(vc, vr, 0, 0)
+
+
+def test_silu_mul(cuda):
+    g = torch.Generator(device=cuda).manual_seed(7)
+    x = torch.randn(61, 2 * 14336, device=cuda, generator=g).bfloat16()
+    _close(ops.silu_mul(x), ref.silu_mul(x.float()), 3e-2)
+
+
+def test_argmax(cuda):
+    g = torch.Generator(device=cuda).manual_seed(8)
+    x = torch.randn(61, 128256, device=cuda, generator=g).bfloat16()
+    x[3, 17] = 100.0
+    x[4, :] = 0
+    got = ops.argmax(x)
+    assert torch.equal(got, x.float().argmax(-1))
+    assert got[4].item() == 0
+
+
+def test_greedy_accept_and_compact(cuda):
+    g = torch.Generator().manual_seed(9)
+    B, T = 4, 61
+    parents = torch.zeros(B, T, dtype=torch.int64)
+    for b in range(B):
+        for t in range(1, T):
+            parents[b, t] = int(torch.randint(0, t, (1,), generator=g))
+    tokens = torch.randint(0, 5, (B, T), generator=g)
+    pred = torch.randint(0, 5, (B, T), generator=g)
+    e_n, e_path, e_out = ref.greedy_accept(tokens, parents, pred)
+    n, path, out = ops.greedy_accept(tokens.to(cuda), parents.to(cuda), pred.to(cuda))
+    assert torch.equal(n.cpu(), e_n)
+    for b in range(B):
+        k = int(e_n[b])
+        assert torch.equal(path[b, : k + 1].cpu(), e_path[b, : k + 1])
+        assert torch.equal(out[b, : k + 1].cpu(), e_out[b, : k + 1])
+    cache = torch.randn(3, 2, B, 2, 128, 128, generator=g).bfloat16()
+    kv_len = torch.tensor([0, 5, 50, 60], dtype=torch.int32)
+    exp = cache.clone()
+    ref.kv_compact(exp, kv_len, e_path, e_n)
+    got = cache.to(cuda)
+    ops.kv_compact(got, kv_len.to(cuda), path, n)
+    assert torch.equal(got.cpu(), exp)
