@@ -1,0 +1,348 @@
+"""Headline benchmark: decode tokens/s + mean accepted length, Llama-3.1-8B + EAGLE-3 dynamic tree on B200.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--batch B] [--impl ours|reference]
+
+One *step* generates ``--new-tokens`` (256) tokens after uniform-random prompts of ``--prompt-len`` (512) tokens for
+``--batch`` rows per GPU through the public API (``EfficientModel.decode_batch``), prefill included. The target is a
+random-init Llama-3.1-8B architecture (bf16, seed 0) and the drafter an EAGLE-3 head (draft vocabulary 32000)
+trained briefly on the target's own greedy continuations of synthetic prompts (``--train-steps``; 0 keeps the
+random head). Decoding: dynamic tree, depth 6, top-k 10, 60 nodes, CUDA graphs.
+
+With N > 1 GPUs (launched by torchrun) every rank serves its own batch (data-parallel replicas; ``scaling``
+"weak"); the step time is the max over ranks of the CUDA-event time. ``value`` is the whole job's generated tokens
+per second. The model weights (16 GB) exceed L2, so every step streams them from HBM (no flush needed).
+
+``--impl reference`` runs the same metric through the unmodified reference (``baseline/_ref``: economize on
+Hugging Face transformers) with the same target and drafter weights.
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+
+import torch
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+METRIC = "decode tok/s + mean accepted len, Llama-3.1-8B EAGLE-3 tree, 1/2/4/8 B200"
+BASELINE_TOKS = None  # BASELINE.md publishes no B200 number for this config
+TREE = {"depth": 6, "topk": 10, "total_tokens": 60}
+
+
+def parse() -> argparse.Namespace:
+    p = argparse.ArgumentParser()
+    p.add_argument("--gpus", type=int, default=1)
+    p.add_argument("--steps", type=int, default=5)
+    p.add_argument("--warmup", type=int, default=3)
+    p.add_argument("--batch", type=int, default=1)
+    p.add_argument("--prompt-len", type=int, default=512)
+    p.add_argument("--new-tokens", type=int, default=256)
+    p.add_argument("--train-steps", type=int, default=0)
+    p.add_argument("--impl", choices=("ours", "reference"), default="ours")
+    p.add_argument("--model", choices=("llama31_8b", "tiny"), default="llama31_8b")
+    p.add_argument("--no-graphs", action="store_true")
+    return p.parse_args()
+
+
+class ClockSampler:
+    """Samples SM clocks and throttle reasons with nvidia-smi while the timed region runs."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, device_index: int) -> None:
+        self.index = device_index
+        self.samples: list[list[str]] = []
+        self._stop = threading.Event()
+        self._thread: threading.Thread | None = None
+
+    def _run(self) -> None:
+        while not self._stop.is_set():
+            try:
+                out = subprocess.run(["nvidia-smi", f"--id={self.index}", f"--query-gpu={self.FIELDS}",
+                                      "--format=csv,noheader,nounits"], capture_output=True, text=True, timeout=5)
+                for line in out.stdout.strip().splitlines():
+                    self.samples.append([x.strip() for x in line.split(",")])
+            except Exception:
+                pass
+            self._stop.wait(0.2)
+
+    def __enter__(self) -> ClockSampler:
+        self._thread = threading.Thread(target=self._run, daemon=True)
+        self._thread.start()
+        return self
+
+    def __exit__(self, *exc) -> None:
+        self._stop.set()
+        if self._thread is not None:
+            self._thread.join(timeout=10)
+
+    def summary(self) -> dict:
+        sm = [float(s[1]) for s in self.samples if len(s) > 8 and s[1].replace(".", "").isdigit()]
+        mx = [float(s[2]) for s in self.samples if len(s) > 8 and s[2].replace(".", "").isdigit()]
+        names = ("hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap")
+        reasons = sorted({n for s in self.samples if len(s) > 8 for n, v in zip(names, s[5:9]) if v == "Active"})
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": max(mx) if mx else None,
+                "reasons": reasons, "samples": len(sm)}
+
+
+def setup_dist(args: argparse.Namespace):
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    if world > 1:
+        import datetime
+
+        import torch.distributed as dist
+
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300),
+                                device_id=torch.device("cuda", local))
+    return world, rank, local
+
+
+def reduce_max(x: float, world: int) -> float:
+    if world == 1:
+        return x
+    import torch.distributed as dist
+
+    t = torch.tensor([x], dtype=torch.float64, device="cuda")
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
+def reduce_sum(x: float, world: int) -> float:
+    if world == 1:
+        return x
+    import torch.distributed as dist
+
+    t = torch.tensor([x], dtype=torch.float64, device="cuda")
+    dist.all_reduce(t)
+    return float(t.item())
+
+
+def barrier(world: int) -> None:
+    if world > 1:
+        import torch.distributed as dist
+
+        dist.barrier()
+
+
+def build_target(args):
+    from economize_b200.models.config import llama31_8b, tiny_llama
+    from economize_b200.models.llama import CausalLM, init_weights
+
+    cfg = llama31_8b() if args.model == "llama31_8b" else tiny_llama(head_dim=128, num_heads=2, num_kv_heads=1)
+    return init_weights(CausalLM(cfg, torch.bfloat16, "cuda"), seed=0)
+
+
+def build_drafter_state(target, args):
+    """EAGLE-3 head weights shared by both arms: seeded init, draft vocabulary = the first 32000 ids, optionally
+    trained on the target's greedy continuations. Returned in the reference's parameter names."""
+    import economize_b200 as eco
+    from economize_b200.techniques.eagle3 import Eagle3Config
+    from economize_b200.techniques.eagle3.formats import to_reference_state
+
+    vocab = min(32000, target.config.vocab_size)
+    em = eco.apply(target, Eagle3Config(draft_vocab=vocab))
+    tech = em.techniques["eagle3"]
+    tech.reset_parameters(seed=1)
+    tech.set_draft_vocab(torch.arange(vocab))
+    if args.train_steps > 0:
+        from economize_b200.train import fit_eagle3_on_greedy
+
+        fit_eagle3_on_greedy(em, steps=args.train_steps, seed=7)
+    return em, to_reference_state(tech)
+
+
+def prompts_for(args, rank: int, vocab: int, device) -> torch.Tensor:
+    g = torch.Generator().manual_seed(1234 + rank)
+    return torch.randint(0, vocab, (args.batch, args.prompt_len), generator=g).to(device)
+
+
+def decode_config(args):
+    import economize_b200 as eco
+
+    return eco.DecodeConfig(cycle_length=TREE["depth"] + 1, draft_policy="dynamic_tree",
+                            draft_policy_options=dict(TREE), cuda_graphs=not args.no_graphs)
+
+
+def acceptance(rows) -> tuple[int, int]:
+    """(accepted drafts, verified cycles) over the rows of one step, for either implementation's results."""
+    accepted = cycles = 0
+    for r in rows:
+        if hasattr(r, "acceptance"):  # the reference: one (drafted, accepted) pair per cycle
+            accepted += sum(a for _, a in r.acceptance)
+            cycles += len(r.acceptance)
+        else:
+            accepted += r.accepted
+            cycles += r.cycles
+    return accepted, cycles
+
+
+def count_launches(step) -> int:
+    """Kernels of this package launched by one step (CUPTI trace of an extra, untimed step)."""
+    from torch.profiler import ProfilerActivity, profile
+
+    names = ("ecz::", "gemm_swapab", "attn_tc", "attn_merge", "rmsnorm_kernel", "rope_store", "silu_mul",
+             "argmax_kernel", "greedy_accept", "kv_compact", "splitk_reduce")
+    with profile(activities=[ProfilerActivity.CUDA]) as prof:
+        step()
+        torch.cuda.synchronize()
+    count = 0
+    for ev in prof.events():
+        if ev.device_type == torch.autograd.DeviceType.CUDA and any(n in ev.name for n in names):
+            count += 1
+    return count
+
+
+def run_ours(args, world, rank):
+    target = build_target(args)
+    em, _ = build_drafter_state(target, args)
+    cfg = decode_config(args)
+    vocab = target.config.vocab_size
+    prompts = prompts_for(args, rank, vocab, "cuda")
+    rows = list(prompts)
+    results = {"cfg": cfg}
+
+    def step():
+        results["r"] = em.decode_batch(rows, args.new_tokens, decoding=cfg)
+
+    return em, step, results, prompts
+
+
+def run_reference(args, world, rank):
+    sys.path.insert(0, os.path.join(HERE, "baseline", "_ref"))
+    try:
+        import economize as ref
+        from economize.techniques.eagle3 import Eagle3Config as RefEagle3Config
+    except Exception as err:  # the install is missing on this box
+        return None, f"reference not importable: {type(err).__name__}: {err}"
+    import transformers
+
+    target = build_target(args)
+    _, dstate = build_drafter_state(target, args)
+    hf_state = target.hf_state_dict()
+    hcfg = target.config.to_hf()
+    del target
+    torch.cuda.empty_cache()
+    with torch.device("cuda"):
+        hf = transformers.LlamaForCausalLM(hcfg).to(torch.bfloat16).eval()
+    hf.load_state_dict(hf_state)
+    del hf_state
+    vocab = hcfg.vocab_size
+    model = ref.apply(hf, RefEagle3Config(draft_vocab=min(32000, vocab), param_dtype="model"))
+    tech = model.techniques["eagle3"]
+    tech.load_state_dict({k: v.to(p.device, p.dtype) for (k, v), p in
+                          zip(dstate.items(), [tech.state_dict()[k] for k in dstate])}, strict=True)
+    cfg = ref.DecodeConfig(cycle_length=TREE["depth"] + 1, draft_policy="dynamic_tree",
+                           draft_policy_options=dict(TREE), cuda_graphs=not args.no_graphs)
+    prompts = prompts_for(args, rank, vocab, "cuda")
+    rows = list(prompts)
+    results = {"cfg": cfg}
+
+    def step():
+        results["r"] = model.decode_batch(rows, args.new_tokens, decoding=cfg)
+
+    return (model, step, results, prompts), None
+
+
+def main() -> None:
+    args = parse()
+    sys.path.insert(0, HERE)
+    if not torch.cuda.is_available():
+        print(json.dumps({"metric": METRIC, "unavailable": "no CUDA device"}))
+        return
+    world, rank, local = setup_dist(args)
+    if args.impl == "reference":
+        built, why = run_reference(args, world, rank)
+        if built is None:
+            if rank == 0:
+                print(json.dumps({"impl": "reference", "unavailable": why}))
+            return
+        model, step, results, prompts = built
+    else:
+        model, step, results, prompts = run_ours(args, world, rank)
+
+    for _ in range(args.warmup):
+        step()
+    torch.cuda.synchronize()
+    barrier(world)
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with ClockSampler(local) as clocks:
+        torch.cuda.synchronize()
+        barrier(world)
+        start.record()
+        for _ in range(args.steps):
+            step()
+        end.record()
+        torch.cuda.synchronize()
+        barrier(world)
+    ms = start.elapsed_time(end) / args.steps
+    ms_max = reduce_max(ms, world)
+    new_tokens = args.batch * args.new_tokens * world
+    value = new_tokens / (ms_max / 1e3)
+    accepted, cycles = acceptance(results["r"])
+    tau_local = 1.0 + accepted / cycles if cycles else None
+
+    # ---- end to end through the public API: pinned host prompts in, host tokens out ----
+    host_prompts = [p.cpu().pin_memory() for p in prompts]
+    e2e_steps = max(1, min(args.steps, 3))
+    torch.cuda.synchronize()
+    barrier(world)
+    t0 = time.perf_counter()
+    for _ in range(e2e_steps):
+        if args.impl == "reference":
+            out = model.decode_batch([p.to("cuda", non_blocking=True) for p in host_prompts], args.new_tokens,
+                                     decoding=results["cfg"])
+        else:
+            out = model.decode_batch(host_prompts, args.new_tokens, decoding=results["cfg"])
+        toks = [r.tokens.cpu() for r in out]
+    torch.cuda.synchronize()
+    e2e_ms = reduce_max((time.perf_counter() - t0) * 1e3 / e2e_steps, world)
+    launches = None
+    if args.impl == "ours":
+        try:
+            launches = count_launches(step) * args.steps
+        except Exception:
+            launches = None
+    tau = None
+    if tau_local is not None:
+        tau = reduce_sum(tau_local, world) / world
+    if rank == 0:
+        line = {
+            "metric": METRIC, "value": round(value, 2), "unit": "tok/s", "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": round(ms_max, 3), "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": (value / BASELINE_TOKS) if BASELINE_TOKS else None, "dtype": "bf16",
+            "data": "synthetic (uniform-random prompts, random-init weights)",
+            "mean_accepted_len": round(tau, 4) if tau is not None else None,
+            "config": {"model": "Llama-3.1-8B arch" if args.model == "llama31_8b" else "tiny",
+                       "drafter": "EAGLE-3 (draft vocab 32000), dynamic tree depth 6 topk 10 nodes 60",
+                       "global_batch": args.batch * world, "seq_len": args.prompt_len,
+                       "new_tokens": args.new_tokens, "parallelism": f"dp{world}",
+                       "train_steps": args.train_steps, "cuda_graphs": not args.no_graphs,
+                       "l2": "weights (16 GB) exceed L2; no flush"},
+            "clocks": clocks.summary(),
+            "e2e": {"value": round(new_tokens / (e2e_ms / 1e3), 2), "unit": "tok/s",
+                    "h2d_bytes_per_step": sum(p.numel() * p.element_size() for p in host_prompts) * world,
+                    "d2h_bytes_per_step": sum(t.numel() * t.element_size() for t in toks) * world},
+            "gpu_launches": launches,
+        }
+        if args.impl == "reference":
+            line["impl"] = "reference"
+        print(json.dumps(line))
+    if world > 1:
+        import torch.distributed as dist
+
+        dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,428 @@
+"""The speculative-decoding engine: a device-resident cycle recorded as one CUDA graph.
+
+economize's ``CycleDecoder`` (``src/economize/decoding/loop.py:57-258``) runs a cycle as Python over Hugging Face
+layers and reads the accepted counts back to the host after every verification (``decoding/commit.py:37-75``); its
+tree verifier loops over nodes on the host (``decoding/verifiers.py:139-158``). Here every step of a cycle is a
+fixed-shape device computation, so the whole cycle is captured once per batch size and replayed:
+
+    draft     root logits -> top-k -> (depth-1) batched tree steps of the drafter -> best ``total_tokens``
+    verify    one target pass over root + tree with 64-bit ancestor masks (tree attention kernel)
+    accept    argmax of the target logits -> longest accepted path (greedy_accept kernel)
+    commit    KV of the accepted path moved to consecutive slots in every layer (kv_compact kernel),
+              tokens appended to the output buffer, lengths advanced
+    observe   the drafter's state for the committed columns + the next root step
+
+The host only polls the generated lengths, every ``n`` cycles where ``n`` is the number of cycles that cannot
+finish any row yet, so no cycle waits on the host.
+"""
+
+from __future__ import annotations
+
+import math
+from dataclasses import dataclass, field
+
+import torch
+
+from .. import ops
+from ..errors import ConfigError
+from ..models.llama import CausalLM
+from ..runtime.cache import KVCache, StepBatch
+from .config import DecodeConfig
+from .drafter import DraftModel
+from .tree import LOGP_FLOOR, TreeOptions, ancestor_bits, chain_parents, popcount64, select_candidates
+
+__all__ = ["DecodeResult", "GenerationStats", "SpecEngine"]
+
+
+@dataclass
+class DecodeResult:
+    """Generated tokens of one row and how they were produced.
+
+    Attributes:
+        tokens: The generated tokens (prompt excluded), truncated at ``max_new_tokens`` and at a stop token.
+        cycles: Exact (verification) passes the row took after the prefill.
+        accepted: Draft tokens accepted over those passes.
+    """
+
+    tokens: torch.Tensor
+    cycles: int = 0
+    accepted: int = 0
+
+    @property
+    def mean_accepted(self) -> float:
+        """Accepted drafts per verified cycle (economize's ``DecodeResult.mean_accepted``)."""
+        return self.accepted / self.cycles if self.cycles else 0.0
+
+    @property
+    def mean_accepted_length(self) -> float:
+        """Tokens committed per exact pass: ``1 + accepted drafts / passes`` (the paper's tau)."""
+        return 1.0 + self.mean_accepted
+
+    def cost_summary(self) -> dict[str, float]:
+        return {"exact_passes": float(self.cycles), "accepted_drafts": float(self.accepted),
+                "mean_accepted_length": self.mean_accepted_length, "new_tokens": float(self.tokens.numel())}
+
+
+@dataclass
+class GenerationStats:
+    cycles: int = 0
+    graph_replays: int = 0
+    host_syncs: int = 0
+    rows: list[DecodeResult] = field(default_factory=list)
+
+    @property
+    def mean_accepted_length(self) -> float:
+        c = sum(r.cycles for r in self.rows)
+        a = sum(r.accepted for r in self.rows)
+        return 1.0 + a / c if c else 1.0
+
+
+class _State:
+    """Persistent device buffers of one (batch, capacity) configuration (graph inputs and outputs)."""
+
+    def __init__(self, model: CausalLM, drafter: DraftModel | None, batch: int, capacity: int, out_cap: int,
+                 draft_vocab: int) -> None:
+        dev = model.device
+        self.batch, self.capacity, self.out_cap = batch, capacity, out_cap
+        self.cache: KVCache = model.new_cache(batch, capacity)
+        i32 = dict(dtype=torch.int32, device=dev)
+        self.kv_len = torch.zeros(batch, **i32)
+        self.last = torch.zeros(batch, dtype=torch.int64, device=dev)
+        self.out = torch.zeros(batch, out_cap + 1, dtype=torch.int64, device=dev)  # last column: trash
+        self.n_out = torch.zeros(batch, **i32)
+        self.max_new = torch.zeros(batch, **i32)
+        self.accepted = torch.zeros(batch, dtype=torch.int64, device=dev)
+        self.cycles = torch.zeros(batch, **i32)
+        hidden = model.config.hidden_size
+        if drafter is not None:
+            self.carry = torch.zeros(batch, max(drafter.carry_size, 1), dtype=model.dtype, device=dev)
+            self.root_logits = torch.zeros(batch, draft_vocab, dtype=torch.float32, device=dev)
+            self.root_state = torch.zeros(batch, hidden, dtype=model.dtype, device=dev)
+
+
+class SpecEngine:
+    """Generates with a target :class:`~economize_b200.models.CausalLM` and an optional drafter.
+
+    Args:
+        model: The target model.
+        drafter: The drafting technique's device-side drafter (``None``: plain decoding).
+        config: Decoding options; ``cycle_length`` drafts per cycle (chains) or ``draft_policy="dynamic_tree"``.
+        draft_vocab: Size of the drafter's vocabulary (for its logits buffer).
+    """
+
+    def __init__(self, model: CausalLM, drafter: DraftModel | None, config: DecodeConfig,
+                 draft_vocab: int | None = None) -> None:
+        self.model = model
+        self.config = config
+        self.drafter = drafter if config.cycle_length > 1 else None
+        self.draft_vocab = draft_vocab or model.config.vocab_size
+        if config.verifier_name not in ("greedy", "accept_all"):
+            raise ConfigError(f"the engine verifies greedily; verifier {config.verifier_name!r} runs through the "
+                              "sampling decoder (economize_b200.decoding.sampling)")
+        self.accept_all = config.verifier_name == "accept_all"
+        policy = config.draft_policy_name
+        self.tree: TreeOptions | None = None
+        if self.drafter is not None and policy == "dynamic_tree":
+            self.tree = TreeOptions.from_options(config.draft_policy_options, config.cycle_length)
+        elif policy not in ("fixed", "confidence", "dynamic_tree"):
+            raise ConfigError(f"unknown draft policy {policy!r}")
+        if self.drafter is None:
+            self.depth = 0
+            self.nodes = 0
+        elif self.tree is not None:
+            self.depth = self.tree.depth
+            self.nodes = self.tree.total_tokens
+        else:
+            self.depth = config.cycle_length - 1
+            self.nodes = self.depth
+        self._states: dict[tuple[int, int, int], _State] = {}
+        self._graphs: dict[tuple[int, int, int], torch.cuda.CUDAGraph] = {}
+        self.stats = GenerationStats()
+
+    # ---- public ------------------------------------------------------------------------------------------------
+    @property
+    def tokens_per_cycle(self) -> int:
+        return self.depth + 1
+
+    def capacity_for(self, prompt_len: int, max_new: int) -> int:
+        slack = self.nodes + 2 + self.depth + (self.tree.forwarded if self.tree else self.depth) + 8
+        return int(math.ceil((prompt_len + max_new + slack) / 128) * 128)
+
+    @torch.no_grad()
+    def generate(self, prompts: list[torch.Tensor] | torch.Tensor, max_new_tokens: int | list[int],
+                 stop_tokens: list[int] | None = None) -> list[DecodeResult]:
+        """Generate after every prompt (1-D tensors of any length, or the rows of a ``[B, P]`` tensor)."""
+        if isinstance(prompts, torch.Tensor):
+            prompts = list(prompts) if prompts.dim() == 2 else [prompts]
+        batch = len(prompts)
+        max_news = [max_new_tokens] * batch if isinstance(max_new_tokens, int) else list(max_new_tokens)
+        longest = max(p.numel() for p in prompts)
+        max_new = max(max_news)
+        capacity = self.capacity_for(longest, max_new)
+        out_cap = max_new + self.depth + 2
+        state = self._state(batch, capacity, out_cap)
+        dev = self.model.device
+        lengths = torch.tensor([p.numel() for p in prompts], dtype=torch.int32)
+        padded = torch.zeros(batch, longest, dtype=torch.int64)
+        for i, p in enumerate(prompts):
+            padded[i, : p.numel()] = p.reshape(-1).cpu()
+        self._prefill(state, padded.to(dev, non_blocking=True), lengths.to(dev, non_blocking=True),
+                      torch.tensor(max_news, dtype=torch.int32).to(dev, non_blocking=True))
+        self._run_cycles(state, max_new, stop_tokens)
+        n_out = state.n_out.cpu()
+        out = state.out[:, :out_cap].cpu()
+        acc = state.accepted.cpu()
+        cyc = state.cycles.cpu()
+        results = []
+        for b in range(batch):
+            toks = out[b, : min(int(n_out[b]), max_news[b])]
+            if stop_tokens:
+                hits = [i for i, t in enumerate(toks.tolist()) if t in stop_tokens]
+                if hits:
+                    toks = toks[: hits[0] + 1]
+            results.append(DecodeResult(toks, int(cyc[b]), int(acc[b])))
+        self.stats.rows = results
+        return results
+
+    # ---- state -------------------------------------------------------------------------------------------------
+    def _state(self, batch: int, capacity: int, out_cap: int) -> _State:
+        key = (batch, capacity, out_cap)
+        st = self._states.get(key)
+        if st is None:
+            # one live configuration at a time keeps memory bounded; graphs of other shapes are dropped
+            self._states = {k: v for k, v in self._states.items() if k[0] == batch}
+            self._graphs = {k: v for k, v in self._graphs.items() if k in self._states}
+            st = _State(self.model, self.drafter, batch, capacity, out_cap, self.draft_vocab)
+            self._states[key] = st
+        else:
+            st.cache.reset()
+            st.n_out.zero_()
+            st.accepted.zero_()
+            st.cycles.zero_()
+        if self.drafter is not None:
+            self.drafter.begin(batch, capacity)
+        return st
+
+    # ---- prefill -----------------------------------------------------------------------------------------------
+    def _prefill(self, st: _State, prompts: torch.Tensor, lengths: torch.Tensor, max_new: torch.Tensor) -> None:
+        model, drafter = self.model, self.drafter
+        batch, width = prompts.shape
+        capture = drafter.capture_layers if drafter is not None else ()
+        chunk = self.config.prefill_chunk
+        if chunk is not None and width > chunk:
+            hidden, aux = self._chunked_prefill(st, prompts, lengths, chunk, capture)
+        else:
+            hidden, aux = model.forward_step(prompts, StepBatch.prefill(lengths, width), st.cache, capture)
+        last_idx = (lengths.long() - 1).clamp_min(0)
+        rows = torch.arange(batch, device=prompts.device)
+        logits = model.logits(hidden[rows, last_idx])
+        bonus = ops.argmax(logits)
+        st.kv_len.copy_(lengths)
+        st.last.copy_(bonus)
+        st.out.zero_()
+        st.out[:, 0] = bonus
+        st.n_out.fill_(1)
+        st.max_new.copy_(max_new)
+        if drafter is not None:
+            fused = drafter.fuse(aux)  # [B, P, d]
+            tokens = torch.cat([prompts, torch.zeros_like(prompts[:, :1])], 1)
+            tokens[rows, lengths.long()] = bonus
+            sources = torch.cat([torch.zeros_like(fused[:, :1]), fused], 1)
+            n_valid = lengths + 1
+            root_logits, root_state = drafter.observe(tokens, sources, torch.zeros_like(lengths), n_valid, lengths)
+            st.root_logits.copy_(root_logits)
+            st.root_state.copy_(root_state)
+            st.carry.copy_(fused[rows, last_idx])
+
+    def _chunked_prefill(self, st: _State, prompts: torch.Tensor, lengths: torch.Tensor, chunk: int,
+                         capture: tuple[int, ...]) -> tuple[torch.Tensor, dict[int, torch.Tensor]]:
+        """Prefill in consecutive causal chunks (activations scale with the chunk, not the prompt)."""
+        batch, width = prompts.shape
+        hs, auxes = [], []
+        for start in range(0, width, chunk):
+            end = min(width, start + chunk)
+            part = prompts[:, start:end]
+            n = (lengths - start).clamp(0, end - start).to(torch.int32)
+            kv = torch.clamp(lengths, max=start).to(torch.int32)
+            pos = (start + torch.arange(end - start, device=prompts.device, dtype=torch.int32)).expand(batch, -1)
+            h, a = self.model.forward_step(part, StepBatch(kv, n, pos.contiguous()), st.cache, capture)
+            hs.append(h)
+            auxes.append(a)
+        hidden = torch.cat(hs, 1)
+        aux = {k: torch.cat([a[k] for a in auxes], 1) for k in auxes[0]}
+        return hidden, aux
+
+    # ---- cycles ------------------------------------------------------------------------------------------------
+    def _run_cycles(self, st: _State, max_new: int, stop_tokens: list[int] | None) -> None:
+        use_graph = self.config.cuda_graphs and self.model.device.type == "cuda"
+        key = (st.batch, st.capacity, st.out_cap)
+        remaining = max_new - 1  # the prefill produced the first token
+        per_cycle = self.tokens_per_cycle
+        while remaining > 0:
+            # cycles that cannot finish any row even if every draft is accepted
+            n = max(1, math.ceil(remaining / per_cycle))
+            for _ in range(n):
+                if use_graph:
+                    graph = self._graphs.get(key)
+                    if graph is None:
+                        self._cycle(st)  # warm-up cycles run eagerly and produce real tokens
+                        self._cycle(st)
+                        graph = self._capture(st)
+                        self._graphs[key] = graph
+                        self.stats.cycles += 2
+                        continue
+                    graph.replay()
+                    self.stats.graph_replays += 1
+                else:
+                    self._cycle(st)
+                self.stats.cycles += 1
+            self.stats.host_syncs += 1
+            done = st.n_out - st.max_new
+            if stop_tokens:
+                hit = torch.isin(st.out[:, : st.out_cap], torch.tensor(stop_tokens, device=st.out.device)).any(1)
+                done = torch.where(hit, torch.zeros_like(done), done)
+            remaining = int(-done.min().item())
+
+    def _capture(self, st: _State) -> torch.cuda.CUDAGraph:
+        graph = torch.cuda.CUDAGraph()
+        torch.cuda.synchronize()
+        with torch.cuda.graph(graph):
+            self._cycle(st, capturing=True)
+        return graph
+
+    def _cycle(self, st: _State, capturing: bool = False) -> None:
+        if self.drafter is None:
+            self._plain_cycle(st)
+        else:
+            self._spec_cycle(st)
+
+    def _plain_cycle(self, st: _State) -> None:
+        model = self.model
+        batch = st.batch
+        one = torch.ones(batch, dtype=torch.int32, device=st.kv_len.device)
+        sb = StepBatch(st.kv_len, one, st.kv_len[:, None].contiguous(),
+                       torch.ones(batch, 1, dtype=torch.int64, device=st.kv_len.device))
+        hidden, _ = model.forward_step(st.last[:, None], sb, st.cache)
+        pred = ops.argmax(model.logits(hidden[:, 0]))
+        active = st.n_out < st.max_new
+        st.out.scatter_(1, torch.where(active, st.n_out, st.out_cap).long()[:, None], pred[:, None])
+        st.n_out.add_(1)
+        st.kv_len.add_(1)
+        st.cycles.add_(active.int())
+        st.last.copy_(pred)
+
+    def _spec_cycle(self, st: _State) -> None:
+        model, drafter = self.model, self.drafter
+        batch, dev = st.batch, st.kv_len.device
+        depth = self.depth
+        if self.tree is not None:
+            draft_tokens, draft_parents = self._draft_tree(st)
+        else:
+            draft_tokens, draft_parents = self._draft_chain(st)
+        # ---- verify: root + drafts in one tree pass ----
+        tokens = torch.cat([st.last[:, None], draft_tokens], 1)  # [B, T]
+        length = tokens.shape[1]
+        parents = torch.cat([torch.zeros(batch, 1, dtype=torch.int64, device=dev), draft_parents + 1], 1)
+        bits = ancestor_bits(parents, depth)
+        positions = (st.kv_len[:, None] + (popcount64(bits) - 1)).to(torch.int32)
+        n_new = torch.full((batch,), length, dtype=torch.int32, device=dev)
+        sb = StepBatch(st.kv_len, n_new, positions, bits)
+        hidden, aux = model.forward_step(tokens, sb, st.cache, drafter.capture_layers)
+        if self.accept_all:
+            pred = ops.argmax(model.logits(hidden))
+            pred = torch.where(torch.arange(length, device=dev)[None] < length - 1,
+                               torch.cat([draft_tokens, pred[:, -1:]], 1), pred)
+        else:
+            pred = ops.argmax(model.logits(hidden))  # [B, T]
+        n_acc, path, out = ops.greedy_accept(tokens, parents, pred)
+        ops.kv_compact(st.cache.data, st.kv_len, path, n_acc)
+        # ---- commit ----
+        active = st.n_out < st.max_new
+        width = depth + 1
+        col = torch.arange(width, device=dev)[None]
+        idx = st.n_out.long()[:, None] + col
+        keep = (col <= n_acc.long()[:, None]) & (idx < st.out_cap) & active[:, None]
+        st.out.scatter_(1, torch.where(keep, idx, st.out_cap), out[:, :width])
+        st.accepted.add_(torch.where(active, n_acc, 0).long())
+        st.cycles.add_(active.int())
+        # ---- observe: drafter state for the committed columns + next root step ----
+        path_w = path[:, :width].long()
+        aux_path = {k: v.gather(1, path_w[..., None].expand(batch, width, v.shape[-1])) for k, v in aux.items()}
+        fused = drafter.fuse(aux_path)  # [B, D+1, d]
+        obs_tokens = torch.cat([st.last[:, None], out[:, :width]], 1)  # [B, D+2]
+        sources = torch.cat([st.carry[:, None].to(fused.dtype), fused], 1)
+        n_valid = (n_acc + 2).to(torch.int32)
+        root_logits, root_state = drafter.observe(obs_tokens, sources, st.kv_len, n_valid, n_valid - 1)
+        rows = torch.arange(batch, device=dev)
+        st.carry.copy_(fused[rows, n_acc.long()])
+        st.last.copy_(out[rows, n_acc.long()])
+        st.kv_len.add_(n_acc + 1)
+        st.n_out.add_(n_acc + 1)
+        st.root_logits.copy_(root_logits)
+        st.root_state.copy_(root_state)
+
+    # ---- drafting ----------------------------------------------------------------------------------------------
+    def _draft_chain(self, st: _State) -> tuple[torch.Tensor, torch.Tensor]:
+        drafter = self.drafter
+        batch, dev = st.batch, st.kv_len.device
+        k = self.depth
+        tok = drafter.to_target(ops.argmax(st.root_logits))
+        tokens = [tok]
+        state = st.root_state[:, None]
+        base = st.kv_len + 1
+        for d in range(1, k):
+            bits = torch.full((batch, 1), (1 << d) - 1, dtype=torch.int64, device=dev)
+            pos = (st.kv_len + d).to(torch.int32)[:, None]
+            logits, out = drafter.tree_step(tok[:, None], state, pos, base, d, d - 1, bits)
+            tok = drafter.to_target(ops.argmax(logits[:, 0]))
+            state = out
+            tokens.append(tok)
+        return torch.stack(tokens, 1), chain_parents(batch, k, dev) - 0
+
+    def _draft_tree(self, st: _State) -> tuple[torch.Tensor, torch.Tensor]:
+        drafter, tree = self.drafter, self.tree
+        batch, dev = st.batch, st.kv_len.device
+        k, depth = tree.topk, tree.depth
+        logp = torch.log_softmax(st.root_logits, -1).clamp_min(LOGP_FLOOR)
+        top = logp.topk(k, -1)
+        f_tokens = drafter.to_target(top.indices)  # frontier tokens [B, k]
+        f_scores = top.values
+        f_cand = torch.arange(k, device=dev).expand(batch, k)
+        cand_tokens, cand_scores = [f_tokens], [f_scores]
+        cand_parents = [torch.full((batch, k), -1, dtype=torch.int64, device=dev)]
+        cand_depth = [torch.zeros(k, device=dev)]
+        states = st.root_state[:, None].expand(batch, k, st.root_state.shape[-1]).contiguous()
+        parent_fwd = torch.full((batch, k), -1, dtype=torch.int64, device=dev)
+        fwd_bits = torch.zeros(batch, max(tree.forwarded, 1), dtype=torch.int64, device=dev)
+        base = st.kv_len + 1
+        for d in range(1, depth):
+            f_idx = (d - 1) * k + torch.arange(k, device=dev)
+            own = torch.ones(batch, k, dtype=torch.int64, device=dev) << f_idx[None]
+            inherited = torch.where(parent_fwd >= 0, fwd_bits.gather(1, parent_fwd.clamp_min(0)),
+                                    torch.zeros_like(own))
+            bits = own | inherited
+            fwd_bits[:, (d - 1) * k: d * k] = bits
+            pos = (st.kv_len + d).to(torch.int32)[:, None].expand(batch, k).contiguous()
+            logits, outs = drafter.tree_step(f_tokens, states, pos, base, d * k, (d - 1) * k, bits)
+            clp = torch.log_softmax(logits, -1).clamp_min(LOGP_FLOOR)
+            ctop = clp.topk(k, -1)
+            child_scores = (f_scores[:, :, None] + ctop.values).reshape(batch, k * k)
+            child_tokens = drafter.to_target(ctop.indices).reshape(batch, k * k)
+            child_parents = f_cand[:, :, None].expand(batch, k, k).reshape(batch, k * k)
+            cand_tokens.append(child_tokens)
+            cand_scores.append(child_scores)
+            cand_parents.append(child_parents)
+            cand_depth.append(torch.full((k * k,), float(d), device=dev))
+            if d < depth - 1:
+                pick = child_scores.topk(k, -1).indices
+                origin = pick // k
+                f_tokens = child_tokens.gather(1, pick)
+                f_scores = child_scores.gather(1, pick)
+                f_cand = k + (d - 1) * k * k + pick
+                parent_fwd = (d - 1) * k + origin
+                states = outs.gather(1, origin[..., None].expand(batch, k, outs.shape[-1]))
+        tokens = torch.cat(cand_tokens, 1)
+        scores = torch.cat(cand_scores, 1)
+        parents = torch.cat(cand_parents, 1)
+        depth_of = torch.cat(cand_depth)
+        return select_candidates(tokens, scores, parents, depth_of, tree.total_tokens)
