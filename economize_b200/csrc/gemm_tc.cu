@@ -217,3 +217,81 @@ int launch_gemm_bf16(const CUtensorMap* tm_w, const CUtensorMap* tm_x, void* y, 
 }
 
 }  // namespace ecz
+
+// ---------------------------------------------------------------------------------------------------------------
+// Allocation-free entry point (see noalloc.h): the split-K partials live in a file-scope device array.
+// ---------------------------------------------------------------------------------------------------------------
+#include <cstdio>
+#include <mutex>
+
+#include "noalloc.h"
+
+namespace {
+
+// fp32 split-K partials, then one status word for the bounded waits.
+static __device__ __align__(256) float g_noalloc_scratch[ECZ_NOALLOC_SCRATCH_FLOATS + 64];
+
+float* noalloc_scratch_for_current_device(int device) {
+  static std::mutex mu;
+  static float* addr[64] = {};
+  if (device < 0 || device >= 64) return nullptr;
+  std::lock_guard<std::mutex> lock(mu);
+  if (addr[device] == nullptr) {
+    void* p = nullptr;
+    const cudaError_t err = cudaGetSymbolAddress(&p, g_noalloc_scratch);
+    if (err != cudaSuccess) {
+      std::fprintf(stderr, "ecz_linear_bf16_noalloc: cudaGetSymbolAddress failed on device %d: %s\n", device,
+                   cudaGetErrorString(err));
+      return nullptr;
+    }
+    addr[device] = static_cast<float*>(p);
+  }
+  return addr[device];
+}
+
+}  // namespace
+
+extern "C" __attribute__((visibility("default"))) int ecz_linear_bf16_noalloc(const void* x, const void* w, void* y,
+                                                                               int M, int N, int K, void* stream) {
+  int device = -1;
+  if (cudaGetDevice(&device) != cudaSuccess) {
+    std::fprintf(stderr, "ecz_linear_bf16_noalloc: no current CUDA device\n");
+    return -5;
+  }
+  if (M <= 0 || N <= 0 || K <= 0 || K % 8 != 0 || N % 4 != 0 ||
+      (reinterpret_cast<uintptr_t>(x) & 15u) || (reinterpret_cast<uintptr_t>(w) & 15u) ||
+      (reinterpret_cast<uintptr_t>(y) & 15u)) {
+    std::fprintf(stderr, "ecz_linear_bf16_noalloc: bad shape or alignment (M=%d N=%d K=%d; K %% 8 and N %% 4 must "
+                 "be 0, pointers 16-byte aligned)\n", M, N, K);
+    return -1;
+  }
+  int sms = 0;
+  cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, device);
+  const int splits = ecz::gemm_splits(M, N, K, sms > 0 ? sms : 148);
+  if (splits > 1 && static_cast<size_t>(splits) * M * N > ECZ_NOALLOC_SCRATCH_FLOATS) {
+    std::fprintf(stderr, "ecz_linear_bf16_noalloc: %d x %d x %d split-K partials need %zu floats, more than the "
+                 "%u-float scratch array\n", splits, M, N, static_cast<size_t>(splits) * M * N,
+                 ECZ_NOALLOC_SCRATCH_FLOATS);
+    return -2;
+  }
+  float* scratch = noalloc_scratch_for_current_device(device);
+  if (scratch == nullptr) return -4;
+  unsigned* status = reinterpret_cast<unsigned*>(scratch + ECZ_NOALLOC_SCRATCH_FLOATS);
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  cudaMemsetAsync(status, 0, sizeof(unsigned), s);  // the status word starts every call cleared
+  CUtensorMap tm_w, tm_x;
+  if (ecz::make_tmap_2d_bf16(&tm_w, w, N, K, K, 128) != 0 ||
+      ecz::make_tmap_2d_bf16(&tm_x, x, M, K, K, ecz::gemm_block_n(M)) != 0) {
+    std::fprintf(stderr, "ecz_linear_bf16_noalloc: cuTensorMapEncodeTiled failed\n");
+    return -3;
+  }
+  if (ecz::launch_gemm_bf16(&tm_w, &tm_x, y, splits > 1 ? scratch : nullptr, M, N, K, splits, status, s) != 0) {
+    return -1;
+  }
+  const cudaError_t err = cudaGetLastError();
+  if (err != cudaSuccess) {
+    std::fprintf(stderr, "ecz_linear_bf16_noalloc: launch failed: %s\n", cudaGetErrorString(err));
+    return -6;
+  }
+  return 0;
+}
