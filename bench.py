@@ -43,7 +43,7 @@ def parse() -> argparse.Namespace:
     p.add_argument("--batch", type=int, default=1)
     p.add_argument("--prompt-len", type=int, default=512)
     p.add_argument("--new-tokens", type=int, default=256)
-    p.add_argument("--train-steps", type=int, default=0)
+    p.add_argument("--train-steps", type=int, default=100)
     p.add_argument("--impl", choices=("ours", "reference"), default="ours")
     p.add_argument("--model", choices=("llama31_8b", "tiny"), default="llama31_8b")
     p.add_argument("--no-graphs", action="store_true")
@@ -143,23 +143,94 @@ def build_target(args):
     return init_weights(CausalLM(cfg, torch.bfloat16, "cuda"), seed=0)
 
 
-def build_drafter_state(target, args):
-    """EAGLE-3 head weights shared by both arms: seeded init, draft vocabulary = the first 32000 ids, optionally
-    trained on the target's greedy continuations. Returned in the reference's parameter names."""
+CACHE_DIR = os.environ.get("ECZ_BENCH_CACHE", "/tmp/economize_b200_bench")
+
+
+def _cache_path(args, rank: int, world: int) -> str:
+    key = f"{args.model}-b{args.batch}-p{args.prompt_len}-n{args.new_tokens}-t{args.train_steps}-r{rank}-w{world}-v2"
+    return os.path.join(CACHE_DIR, f"drafter-{key}.pt")
+
+
+def reference_module():
+    """The installed reference package (``baseline/_ref``), or ``None``."""
+    ref_dir = os.path.join(HERE, "baseline", "_ref")
+    if not os.path.isdir(os.path.join(ref_dir, "economize")):
+        return None
+    if ref_dir not in sys.path:
+        sys.path.insert(0, ref_dir)
+    try:
+        import economize
+
+        return economize
+    except Exception:
+        return None
+
+
+def hf_twin(target):
+    """A ``transformers`` Llama with the target's weights (bf16, on the GPU)."""
+    import transformers
+
+    hcfg = target.config.to_hf()
+    with torch.device("cuda"):
+        hf = transformers.LlamaForCausalLM(hcfg).to(torch.bfloat16).eval()
+    hf.load_state_dict(target.hf_state_dict())
+    return hf
+
+
+def plain_continuations_ref(ref, hf, prompts, new_tokens):
+    model = ref.apply(hf)
+    out = model.decode_batch(list(prompts), new_tokens, decoding=ref.DecodeConfig(cycle_length=1))
+    rows = torch.stack([torch.cat([p, r.tokens.to(p.device)]) for p, r in zip(prompts, out)])
+    model.detach()
+    return rows
+
+
+def build_drafter(target, args, rank: int, world: int, prompts, hf=None):
+    """EAGLE-3 head weights shared by both arms, in the reference's parameter names.
+
+    The random-init target's greedy continuation is chaotic, so a drafter can only be accurate where it has seen
+    the continuation: it is trained (``--train-steps``) on the plain greedy continuations of the benchmark prompts
+    produced by BOTH implementations (each arm's own bf16 rounding leads to its own trajectory), starting from an
+    early-exit initialisation (fc picks the highest feature, the layer passes it through, the head is the target's
+    restricted to the 32000 most frequent continuation tokens). The result is cached on the box, so the arm that
+    runs second loads exactly the weights the first one trained.
+    """
     import economize_b200 as eco
     from economize_b200.techniques.eagle3 import Eagle3Config
-    from economize_b200.techniques.eagle3.formats import to_reference_state
+    from economize_b200.techniques.eagle3.formats import from_reference_state, to_reference_state
 
     vocab = min(32000, target.config.vocab_size)
     em = eco.apply(target, Eagle3Config(draft_vocab=vocab))
     tech = em.techniques["eagle3"]
-    tech.reset_parameters(seed=1)
-    tech.set_draft_vocab(torch.arange(vocab))
+    path = _cache_path(args, rank, world)
+    if os.path.exists(path):
+        from_reference_state(tech, torch.load(path, map_location="cuda", weights_only=True))
+        return em, to_reference_state(tech)
+    tech.reset_parameters(seed=1, identity=True)
     if args.train_steps > 0:
-        from economize_b200.train import fit_eagle3_on_greedy
+        from economize_b200.train import fit
 
-        fit_eagle3_on_greedy(em, steps=args.train_steps, seed=7)
-    return em, to_reference_state(tech)
+        plain = em.decode_batch(list(prompts), args.new_tokens,
+                                decoding=eco.DecodeConfig(cycle_length=1, cuda_graphs=True))
+        rows = [torch.stack([torch.cat([p, r.tokens.to(p.device)]) for p, r in zip(prompts, plain)])]
+        ref = reference_module()
+        if ref is not None:
+            own_hf = hf is None
+            hf = hf if hf is not None else hf_twin(target)
+            rows.append(plain_continuations_ref(ref, hf, prompts, args.new_tokens))
+            if own_hf:
+                del hf
+                torch.cuda.empty_cache()
+        data = torch.cat(rows)
+        tech.draft_vocab_from(data[:, args.prompt_len:])
+        fit(em, data, steps=args.train_steps, batch_size=min(4, data.shape[0]), seed=0, lr=1e-3, warmup_steps=5,
+            log_every=max(1, args.train_steps))
+    state = to_reference_state(tech)
+    os.makedirs(CACHE_DIR, exist_ok=True)
+    tmp = path + f".{os.getpid()}.tmp"
+    torch.save({k: v.cpu() for k, v in state.items()}, tmp)
+    os.replace(tmp, path)
+    return em, state
 
 
 def prompts_for(args, rank: int, vocab: int, device) -> torch.Tensor:
@@ -205,10 +276,10 @@ def count_launches(step) -> int:
 
 def run_ours(args, world, rank):
     target = build_target(args)
-    em, _ = build_drafter_state(target, args)
-    cfg = decode_config(args)
     vocab = target.config.vocab_size
     prompts = prompts_for(args, rank, vocab, "cuda")
+    em, _ = build_drafter(target, args, rank, world, prompts)
+    cfg = decode_config(args)
     rows = list(prompts)
     results = {"cfg": cfg}
 
@@ -219,32 +290,24 @@ def run_ours(args, world, rank):
 
 
 def run_reference(args, world, rank):
-    sys.path.insert(0, os.path.join(HERE, "baseline", "_ref"))
-    try:
-        import economize as ref
-        from economize.techniques.eagle3 import Eagle3Config as RefEagle3Config
-    except Exception as err:  # the install is missing on this box
-        return None, f"reference not importable: {type(err).__name__}: {err}"
-    import transformers
+    ref = reference_module()
+    if ref is None:
+        return None, "reference not importable from baseline/_ref"
+    from economize.techniques.eagle3 import Eagle3Config as RefEagle3Config
 
     target = build_target(args)
-    _, dstate = build_drafter_state(target, args)
-    hf_state = target.hf_state_dict()
-    hcfg = target.config.to_hf()
-    del target
+    vocab = target.config.vocab_size
+    prompts = prompts_for(args, rank, vocab, "cuda")
+    hf = hf_twin(target)
+    _, dstate = build_drafter(target, args, rank, world, prompts, hf=hf)
+    del target, _
     torch.cuda.empty_cache()
-    with torch.device("cuda"):
-        hf = transformers.LlamaForCausalLM(hcfg).to(torch.bfloat16).eval()
-    hf.load_state_dict(hf_state)
-    del hf_state
-    vocab = hcfg.vocab_size
     model = ref.apply(hf, RefEagle3Config(draft_vocab=min(32000, vocab), param_dtype="model"))
     tech = model.techniques["eagle3"]
-    tech.load_state_dict({k: v.to(p.device, p.dtype) for (k, v), p in
-                          zip(dstate.items(), [tech.state_dict()[k] for k in dstate])}, strict=True)
+    current = tech.state_dict()
+    tech.load_state_dict({k: v.to(current[k].device, current[k].dtype) for k, v in dstate.items()}, strict=True)
     cfg = ref.DecodeConfig(cycle_length=TREE["depth"] + 1, draft_policy="dynamic_tree",
                            draft_policy_options=dict(TREE), cuda_graphs=not args.no_graphs)
-    prompts = prompts_for(args, rank, vocab, "cuda")
     rows = list(prompts)
     results = {"cfg": cfg}
 
@@ -324,7 +387,9 @@ def main() -> None:
             "data": "synthetic (uniform-random prompts, random-init weights)",
             "mean_accepted_len": round(tau, 4) if tau is not None else None,
             "config": {"model": "Llama-3.1-8B arch" if args.model == "llama31_8b" else "tiny",
-                       "drafter": "EAGLE-3 (draft vocab 32000), dynamic tree depth 6 topk 10 nodes 60",
+                       "drafter": "EAGLE-3 (draft vocab 32000), dynamic tree depth 6 topk 10 nodes 60; trained "
+                                  f"{args.train_steps} steps on both implementations' plain greedy continuations of "
+                                  "the benchmark prompts (same weights in both arms)",
                        "global_batch": args.batch * world, "seq_len": args.prompt_len,
                        "new_tokens": args.new_tokens, "parallelism": f"dp{world}",
                        "train_steps": args.train_steps, "cuda_graphs": not args.no_graphs,

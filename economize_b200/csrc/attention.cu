@@ -29,7 +29,7 @@ constexpr int kKeys = 128;
 constexpr int kDim = 128;
 constexpr int kAtom = kRows * 128;          // bytes of one 64-column swizzled half tile (128 rows x 128 B)
 constexpr int kTile = 2 * kAtom;            // a 128 x 128 bf16 tile
-constexpr int kSmem = 6 * kTile + 1024 + 256;  // Q, P, 2 x K, 2 x V
+constexpr int kSmem = 6 * kTile + 1024 + 64 + 4 * 128 * 4;  // Q, P, 2 x K, 2 x V, barriers, row partials
 
 __device__ __forceinline__ void store_row_swizzled(uint8_t* tile, int r, int chunk, uint4 v) {
   // chunk in [0, 16): 16-byte chunk of a 256-byte row; chunks 0-7 in the first half tile, 8-15 in the second
@@ -38,12 +38,44 @@ __device__ __forceinline__ void store_row_swizzled(uint8_t* tile, int r, int chu
   *reinterpret_cast<uint4*>(atom + r * 128 + ((c ^ (r & 7)) << 4)) = v;
 }
 
-__global__ void __launch_bounds__(128, 1)
+// Visibility of the 32 slots [s0, s0 + 32) for one query row, bit i = slot s0 + i.
+__device__ __forceinline__ uint32_t visible32(int s0, int base, int nn, bool use_mask, uint64_t bits, int causal_lim,
+                                              bool row_valid) {
+  if (!row_valid) return 0u;
+  const int pre = min(max(base - s0, 0), 32);  // committed prefix
+  uint32_t vis = pre >= 32 ? 0xffffffffu : ((1u << pre) - 1u);
+  const int j0 = s0 - base;  // new-region index of slot s0
+  const int lim = use_mask ? min(nn, 64) : min(nn, causal_lim);
+  const int hi = min(lim - j0, 32);  // bits i < hi have j < lim
+  const int lo = max(-j0, 0);        // bits i >= lo have j >= 0
+  if (hi > lo) {
+    uint32_t range = (hi >= 32 ? 0xffffffffu : ((1u << hi) - 1u)) & ~(lo >= 32 ? 0xffffffffu : ((1u << lo) - 1u));
+    uint32_t sel = 0xffffffffu;
+    if (use_mask) {
+      const uint64_t w = j0 >= 0 ? (j0 < 64 ? (bits >> j0) : 0ull) : (-j0 < 64 ? (bits << (-j0)) : 0ull);
+      sel = static_cast<uint32_t>(w);
+    }
+    vis |= range & sel;
+  }
+  return vis;
+}
+
+__device__ __forceinline__ float fast_exp2(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+
+// 16 warps: warp w reads TMEM lanes 32 * (w % 4) .. (its rows) and owns score / output columns
+// [32 * (w / 4), 32 * (w / 4) + 32) of them (quarter q).
+constexpr int kThreads = 512;
+
+__global__ void __launch_bounds__(kThreads, 1)
     attn_tc_kernel(const bf16* __restrict__ q, const __grid_constant__ CUtensorMap tm_k,
                    const __grid_constant__ CUtensorMap tm_v, bf16* __restrict__ out, float* __restrict__ ws_o,
                    float* __restrict__ ws_ml, const int* __restrict__ kv_len, const int* __restrict__ n_new,
                    const int64_t* __restrict__ mask, int T, int H, int Hkv, int S, float scale_log2, int q_offset,
-                   int chunks_per_split, int m_tiles, unsigned* status) {
+                   int chunks_per_split, int m_tiles, unsigned* status, unsigned long long* trace) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* q_tile = smem;
@@ -55,59 +87,41 @@ __global__ void __launch_bounds__(128, 1)
   uint64_t* bar_pv = bar_s + 1;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bar_pv + 1);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+  float* red = reinterpret_cast<float*>(smem + 6 * kTile + 64);  // [4][128] row partials
 
-  const int tid = threadIdx.x, warp = tid >> 5;
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int quad = warp & 3, quarter = warp >> 2;
+  const int r = quad * 32 + lane;  // this thread's row (TMEM lane)
+  unsigned long long* stamp = (trace != nullptr && tid == 0)
+                                  ? trace + (static_cast<size_t>(blockIdx.y) * gridDim.x + blockIdx.x) * 8
+                                  : nullptr;
+  if (stamp) stamp[0] = global_timer_ns();
+  pdl_trigger();
+  pdl_wait();
   const int m_tile = blockIdx.x % m_tiles;
   const int bh = blockIdx.x / m_tiles;
   const int b = bh / Hkv, kvh = bh % Hkv;
   const int split = blockIdx.y, splits = gridDim.y;
   const int G = H / Hkv;
 
-  // this thread's query row
-  const int p = m_tile * kRows + tid;
+  const int p = m_tile * kRows + r;
   const int t = p / G;
   const int head = kvh * G + p % G;
   const bool row_valid = t < T;
   const int base = kv_len[b];
   const int nn = n_new[b];
-  const uint64_t bits = (row_valid && mask != nullptr) ? static_cast<uint64_t>(mask[static_cast<size_t>(b) * T + t])
-                                                       : 0ull;
+  const bool use_mask = mask != nullptr;
+  const uint64_t bits = (row_valid && use_mask) ? static_cast<uint64_t>(mask[static_cast<size_t>(b) * T + t]) : 0ull;
+  const int causal_lim = q_offset + t + 1;
 
-  // key chunks this CTA covers: up to the last slot any row of the tile may see
-  int t_last = std::min(T - 1, ((m_tile + 1) * kRows - 1) / G);
-  int visible_end = mask != nullptr ? base + nn : base + std::min(nn, q_offset + t_last + 1);
-  visible_end = std::min(visible_end, S);
+  const int t_last = min(T - 1, ((m_tile + 1) * kRows - 1) / G);
+  int visible_end = use_mask ? base + nn : base + min(nn, q_offset + t_last + 1);
+  visible_end = min(visible_end, S);
   const int n_chunks = (visible_end + kKeys - 1) / kKeys;
   const int c0 = split * chunks_per_split;
-  const int c1 = std::min(n_chunks, c0 + chunks_per_split);
+  const int c1 = min(n_chunks, c0 + chunks_per_split);
 
-  if (tid == 0) {
-    mbar_init(&kv_full[0], 1);
-    mbar_init(&kv_full[1], 1);
-    mbar_init(bar_s, 1);
-    mbar_init(bar_pv, 1);
-    *abort_flag = 0;
-    fence_mbar_init();
-  }
-  __syncwarp();
-  if (warp == 0) tmem_alloc(tmem_slot, 256);
-
-  // Q row -> swizzled K-major tile (zeros for padding rows)
-  {
-    const uint4* src = reinterpret_cast<const uint4*>(q + (static_cast<size_t>(b) * T + t) * H * kDim +
-                                                      static_cast<size_t>(head) * kDim);
-#pragma unroll
-    for (int c = 0; c < 16; ++c) store_row_swizzled(q_tile, tid, c, row_valid ? src[c] : make_uint4(0, 0, 0, 0));
-  }
-  fence_async_smem();
-  tc_fence_before();
-  __syncthreads();
-  tc_fence_after();
-  const uint32_t tmem = *tmem_slot;
-  const uint32_t tmem_s = tmem, tmem_pv = tmem + 128;
-  const uint32_t lane_off = static_cast<uint32_t>(warp * 32) << 16;
   const size_t kv_row0 = (static_cast<size_t>(b) * Hkv + kvh) * S;
-
   auto issue_kv = [&](int c, int s) {
     mbar_arrive_expect_tx(&kv_full[s], 4 * kAtom);
     const int y = static_cast<int>(kv_row0 + static_cast<size_t>(c) * kKeys);
@@ -117,13 +131,42 @@ __global__ void __launch_bounds__(128, 1)
     tma_load_2d(v_tiles + s * kTile + kAtom, &tm_v, &kv_full[s], 64, y);
   };
   if (tid == 0) {
+    mbar_init(&kv_full[0], 1);
+    mbar_init(&kv_full[1], 1);
+    mbar_init(bar_s, 1);
+    mbar_init(bar_pv, 1);
+    *abort_flag = 0;
+    fence_mbar_init();
+    // the first two K/V chunks stream while the CTA allocates TMEM and stages Q
     if (c0 < c1) issue_kv(c0, 0);
     if (c0 + 1 < c1) issue_kv(c0 + 1, 1);
   }
+  __syncwarp();
+  if (warp == 0) tmem_alloc(tmem_slot, 256);
 
-  float o[kDim];
+  // Q row r, chunks [4 * quarter, 4 * quarter + 4) -> swizzled K-major tile (zeros for padding rows)
+  {
+    const uint4* src = reinterpret_cast<const uint4*>(q + (static_cast<size_t>(b) * T + t) * H * kDim +
+                                                      static_cast<size_t>(head) * kDim);
 #pragma unroll
-  for (int d = 0; d < kDim; ++d) o[d] = 0.f;
+    for (int c = 0; c < 4; ++c) {
+      const int chunk = quarter * 4 + c;
+      store_row_swizzled(q_tile, r, chunk, row_valid ? src[chunk] : make_uint4(0, 0, 0, 0));
+    }
+  }
+  fence_async_smem();
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+  if (stamp) stamp[1] = global_timer_ns();
+  const uint32_t lane_off = static_cast<uint32_t>(quad * 32) << 16;
+  const uint32_t col0 = quarter * 32;
+  const uint32_t tmem_s = tmem + col0, tmem_pv = tmem + 128 + col0;
+
+  float o[32];
+#pragma unroll
+  for (int d = 0; d < 32; ++d) o[d] = 0.f;
   float m_run = -INFINITY, l_run = 0.f;
   constexpr uint32_t idesc_s = idesc_bf16_f32(kRows, kKeys);
   constexpr uint32_t idesc_pv = idesc_bf16_f32(kRows, kDim, /*b_mn_major=*/true);
@@ -136,13 +179,14 @@ __global__ void __launch_bounds__(128, 1)
     const uint32_t ph = i & 1;
     ok = mbar_wait(&kv_full[s], kv_phase, status, kStatusWaitFull, abort_flag);
     if (!ok) break;
+    if (stamp && i == 0) stamp[2] = global_timer_ns();
     if (tid == 0) {
       tc_fence_after();
       const uint32_t qa = smem_u32(q_tile), ka = smem_u32(k_tiles + s * kTile);
 #pragma unroll
       for (int kk = 0; kk < kDim / 16; ++kk) {
         const uint32_t off = (kk >> 2) * kAtom + (kk & 3) * 32;
-        umma_bf16(tmem_s, desc_kmajor_sw128(qa + off), desc_kmajor_sw128(ka + off), idesc_s, kk != 0);
+        umma_bf16(tmem, desc_kmajor_sw128(qa + off), desc_kmajor_sw128(ka + off), idesc_s, kk != 0);
       }
       umma_commit(bar_s);
     }
@@ -151,52 +195,42 @@ __global__ void __launch_bounds__(128, 1)
     if (!ok) break;
     __syncwarp();
     tc_fence_after();
+    if (stamp && i == 0) stamp[3] = global_timer_ns();
 
-    // pass 1: masked row max of this chunk
-    const int slot0 = c * kKeys;
-    float cmax = -INFINITY;
-#pragma unroll 1
-    for (int cc = 0; cc < kKeys; cc += 16) {
-      float v[16];
-      tmem_ld16(tmem_s + lane_off + cc, v);
+    // this thread's 32 scores of the chunk
+    float sc[32];
+    tmem_ld16(tmem_s + lane_off, sc);
+    tmem_ld16(tmem_s + lane_off + 16, sc + 16);
+    const uint32_t vis = visible32(c * kKeys + col0, base, nn, use_mask, bits, causal_lim, row_valid);
+    float qmax = -INFINITY;
 #pragma unroll
-      for (int j = 0; j < 16; ++j) {
-        const int slot = slot0 + cc + j;
-        const int jn = slot - base;
-        bool vis = row_valid && (slot < base || (jn < nn && (mask != nullptr ? (jn < 64 && ((bits >> jn) & 1ull) != 0ull)
-                                                                             : jn <= q_offset + t)));
-        if (vis) cmax = fmaxf(cmax, v[j] * scale_log2);
-      }
+    for (int j = 0; j < 32; ++j) {
+      sc[j] *= scale_log2;
+      if ((vis >> j) & 1u) qmax = fmaxf(qmax, sc[j]);
     }
+    red[quarter * kRows + r] = qmax;
+    __syncthreads();
+    const float cmax = fmaxf(fmaxf(red[r], red[kRows + r]), fmaxf(red[2 * kRows + r], red[3 * kRows + r]));
     const float m_new = fmaxf(m_run, cmax);
-    const float alpha = m_new == -INFINITY ? 1.f : exp2f(m_run - m_new);
-    // pass 2: probabilities -> bf16 P tile, running sum
+    const float alpha = m_new == -INFINITY ? 1.f : fast_exp2(m_run - m_new);
     float csum = 0.f;
-#pragma unroll 1
-    for (int cc = 0; cc < kKeys; cc += 16) {
-      float v[16];
-      tmem_ld16(tmem_s + lane_off + cc, v);
-      uint32_t packed[8];
+    uint32_t packed[16];
 #pragma unroll
-      for (int j = 0; j < 16; j += 2) {
-        float pr[2];
+    for (int j = 0; j < 32; j += 2) {
+      const float p0 = ((vis >> j) & 1u) ? fast_exp2(sc[j] - m_new) : 0.f;
+      const float p1 = ((vis >> (j + 1)) & 1u) ? fast_exp2(sc[j + 1] - m_new) : 0.f;
+      __nv_bfloat162 h2 = __floats2bfloat162_rn(p0, p1);
+      csum += __bfloat162float(h2.x) + __bfloat162float(h2.y);  // the sum of what P . V multiplies
+      packed[j / 2] = *reinterpret_cast<uint32_t*>(&h2);
+    }
 #pragma unroll
-        for (int u = 0; u < 2; ++u) {
-          const int slot = slot0 + cc + j + u;
-          const int jn = slot - base;
-          bool vis = row_valid && (slot < base || (jn < nn && (mask != nullptr ? (jn < 64 && ((bits >> jn) & 1ull) != 0ull)
-                                                                               : jn <= q_offset + t)));
-          pr[u] = vis ? exp2f(v[j + u] * scale_log2 - m_new) : 0.f;
-        }
-        __nv_bfloat162 h2 = __floats2bfloat162_rn(pr[0], pr[1]);
-        csum += __bfloat162float(h2.x) + __bfloat162float(h2.y);  // the sum of what P . V multiplies
-        packed[j / 2] = *reinterpret_cast<uint32_t*>(&h2);
-      }
-      store_row_swizzled(p_tile, tid, cc / 8, make_uint4(packed[0], packed[1], packed[2], packed[3]));
-      store_row_swizzled(p_tile, tid, cc / 8 + 1, make_uint4(packed[4], packed[5], packed[6], packed[7]));
+    for (int u = 0; u < 4; ++u) {
+      store_row_swizzled(p_tile, r, quarter * 4 + u,
+                         make_uint4(packed[4 * u], packed[4 * u + 1], packed[4 * u + 2], packed[4 * u + 3]));
     }
     l_run = l_run * alpha + csum;
     m_run = m_new;
+    if (stamp && i == 0) stamp[4] = global_timer_ns();
     fence_async_smem();
     tc_fence_before();
     __syncthreads();
@@ -206,7 +240,7 @@ __global__ void __launch_bounds__(128, 1)
 #pragma unroll
       for (int kk = 0; kk < kKeys / 16; ++kk) {
         const uint32_t a_off = (kk >> 2) * kAtom + (kk & 3) * 32;
-        umma_bf16(tmem_pv, desc_kmajor_sw128(pa + a_off), desc_mnmajor_sw128(va + kk * 2048, kAtom), idesc_pv,
+        umma_bf16(tmem + 128, desc_kmajor_sw128(pa + a_off), desc_mnmajor_sw128(va + kk * 2048, kAtom), idesc_pv,
                   kk != 0);
       }
       umma_commit(bar_pv);
@@ -214,27 +248,32 @@ __global__ void __launch_bounds__(128, 1)
     __syncwarp();
     ok = mbar_wait(bar_pv, ph, status, kStatusWaitAccum, abort_flag);
     if (!ok) break;
+    __syncwarp();
     tc_fence_after();
+    if (stamp && i == 0) stamp[5] = global_timer_ns();
     if (tid == 0 && c + 2 < c1) issue_kv(c + 2, s);  // both MMAs reading stage s are done
     __syncwarp();
+    float pv[32];
+    tmem_ld16(tmem_pv + lane_off, pv);
+    tmem_ld16(tmem_pv + lane_off + 16, pv + 16);
 #pragma unroll
-    for (int cc = 0; cc < kDim; cc += 16) {
-      float v[16];
-      tmem_ld16(tmem_pv + lane_off + cc, v);
-#pragma unroll
-      for (int j = 0; j < 16; ++j) o[cc + j] = o[cc + j] * alpha + v[j];
-    }
+    for (int d = 0; d < 32; ++d) o[d] = o[d] * alpha + pv[d];
   }
+  if (stamp) stamp[6] = global_timer_ns();
   tc_fence_before();
   __syncthreads();
   const bool failed = *abort_flag != 0;
+  // row sum over the four quarters
+  red[quarter * kRows + r] = l_run;
+  __syncthreads();
+  const float l_tot = red[r] + red[kRows + r] + red[2 * kRows + r] + red[3 * kRows + r];
 
   if (!failed && row_valid) {
     if (splits == 1) {
-      const float inv = l_run > 0.f ? 1.f / l_run : 0.f;
-      uint4* dst = reinterpret_cast<uint4*>(out + ((static_cast<size_t>(b) * T + t) * H + head) * kDim);
+      const float inv = l_tot > 0.f ? 1.f / l_tot : 0.f;
+      uint4* dst = reinterpret_cast<uint4*>(out + ((static_cast<size_t>(b) * T + t) * H + head) * kDim + col0);
 #pragma unroll
-      for (int c = 0; c < 16; ++c) {
+      for (int c = 0; c < 4; ++c) {
         uint32_t w[4];
 #pragma unroll
         for (int u = 0; u < 4; ++u) {
@@ -244,21 +283,26 @@ __global__ void __launch_bounds__(128, 1)
         dst[c] = make_uint4(w[0], w[1], w[2], w[3]);
       }
     } else {
-      const size_t slot = (static_cast<size_t>(blockIdx.x) * splits + split) * kRows + tid;
-      float4* dst = reinterpret_cast<float4*>(ws_o + slot * kDim);
+      const size_t slot = (static_cast<size_t>(blockIdx.x) * splits + split) * kRows + r;
+      float4* dst = reinterpret_cast<float4*>(ws_o + slot * kDim + col0);
 #pragma unroll
-      for (int c = 0; c < kDim / 4; ++c) dst[c] = make_float4(o[4 * c], o[4 * c + 1], o[4 * c + 2], o[4 * c + 3]);
-      ws_ml[slot * 2] = m_run;
-      ws_ml[slot * 2 + 1] = l_run;
+      for (int c = 0; c < 8; ++c) dst[c] = make_float4(o[4 * c], o[4 * c + 1], o[4 * c + 2], o[4 * c + 3]);
+      if (quarter == 0) {
+        ws_ml[slot * 2] = m_run;
+        ws_ml[slot * 2 + 1] = l_tot;
+      }
     }
   }
   if (warp == 0) tmem_dealloc(tmem, 256);
+  if (stamp) stamp[7] = global_timer_ns();
 }
 
 // Combine the split partials of every packed row: out = sum_s O_s 2^(m_s - M) / sum_s l_s 2^(m_s - M).
 __global__ void __launch_bounds__(128) attn_merge_kernel(const float* __restrict__ ws_o,
                                                          const float* __restrict__ ws_ml, bf16* __restrict__ out,
                                                          int T, int H, int Hkv, int m_tiles, int splits) {
+  pdl_trigger();
+  pdl_wait();
   const int tile = blockIdx.x;  // (b * Hkv + kvh) * m_tiles + m_tile
   const int r = blockIdx.y * 4 + (threadIdx.x >> 5);
   const int lane = threadIdx.x & 31;
@@ -293,23 +337,27 @@ __global__ void __launch_bounds__(128) attn_merge_kernel(const float* __restrict
 
 }  // namespace
 
+// The split over keys depends on the batch, the KV heads and the cache size only (not on the number of query
+// tokens), so a one-token pass and a verification pass reduce a row's keys in the same order.
 AttnPlan attention_plan(int B, int T, int H, int Hkv, int S, int num_sms) {
   AttnPlan plan;
   const int G = H / Hkv;
   plan.m_tiles = (T * G + kRows - 1) / kRows;
   const int total_chunks = (S + kKeys - 1) / kKeys;
-  const int ctas = B * Hkv * plan.m_tiles;
+  const int heads = B * Hkv;
   int splits = 1;
-  if (ctas < num_sms) splits = std::min(total_chunks, std::max(1, (2 * num_sms) / ctas));
+  if (heads < num_sms) splits = std::min(total_chunks, std::max(1, (2 * num_sms) / heads));
   plan.chunks_per_split = (total_chunks + splits - 1) / splits;
   plan.splits = (total_chunks + plan.chunks_per_split - 1) / plan.chunks_per_split;
-  plan.ws_floats = plan.splits > 1 ? static_cast<long>(ctas) * plan.splits * kRows * (kDim + 2) : 0;
+  const long ctas = static_cast<long>(heads) * plan.m_tiles;
+  plan.ws_floats = plan.splits > 1 ? ctas * plan.splits * kRows * (kDim + 2) : 0;
   return plan;
 }
 
 int launch_attention(const void* q, const CUtensorMap* tm_k, const CUtensorMap* tm_v, void* out, float* ws,
                      const int* kv_len, const int* n_new, const int64_t* mask, int B, int T, int H, int Hkv, int D,
-                     int S, float scale, int q_offset, const AttnPlan& plan, unsigned* status, cudaStream_t stream) {
+                     int S, float scale, int q_offset, const AttnPlan& plan, unsigned* status, cudaStream_t stream,
+                     unsigned long long* trace) {
   if (D != kDim || H % Hkv != 0) return -1;
   if (mask != nullptr && T > 64) return -1;
   static bool configured = false;
@@ -321,14 +369,13 @@ int launch_attention(const void* q, const CUtensorMap* tm_k, const CUtensorMap* 
   float* ws_o = plan.splits > 1 ? ws : nullptr;
   float* ws_ml = plan.splits > 1 ? ws + static_cast<size_t>(ctas) * plan.splits * kRows * kDim : nullptr;
   dim3 grid(ctas, plan.splits);
-  attn_tc_kernel<<<grid, 128, kSmem, stream>>>(static_cast<const bf16*>(q), *tm_k, *tm_v, static_cast<bf16*>(out),
-                                               ws_o, ws_ml, kv_len, n_new, mask, T, H, Hkv, S,
-                                               scale * 1.4426950408889634f, q_offset, plan.chunks_per_split,
-                                               plan.m_tiles, status);
+  launch_pdl(attn_tc_kernel, grid, dim3(kThreads), kSmem, stream, static_cast<const bf16*>(q), *tm_k, *tm_v,
+             static_cast<bf16*>(out), ws_o, ws_ml, kv_len, n_new, mask, T, H, Hkv, S, scale * 1.4426950408889634f,
+             q_offset, plan.chunks_per_split, plan.m_tiles, status, trace);
   if (plan.splits > 1) {
     dim3 mgrid(ctas, kRows / 4);
-    attn_merge_kernel<<<mgrid, 128, 0, stream>>>(ws_o, ws_ml, static_cast<bf16*>(out), T, H, Hkv, plan.m_tiles,
-                                                 plan.splits);
+    launch_pdl(attn_merge_kernel, mgrid, dim3(128), 0, stream, static_cast<const float*>(ws_o),
+               static_cast<const float*>(ws_ml), static_cast<bf16*>(out), T, H, Hkv, plan.m_tiles, plan.splits);
   }
   return 0;
 }

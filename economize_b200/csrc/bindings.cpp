@@ -45,6 +45,19 @@ unsigned* status_word(const at::Device& device) {
   return reinterpret_cast<unsigned*>(it->second.data_ptr<int>());
 }
 
+// Split-K tile counters (zeroed once, reset by the kernels) private to each (device, stream).
+int* split_counters(const at::Device& device, cudaStream_t stream) {
+  static std::mutex mu;
+  static std::unordered_map<uint64_t, Tensor> bufs;
+  std::lock_guard<std::mutex> lock(mu);
+  const uint64_t key = (static_cast<uint64_t>(device.index()) << 56) ^ reinterpret_cast<uint64_t>(stream);
+  auto it = bufs.find(key);
+  if (it == bufs.end()) {
+    it = bufs.emplace(key, at::zeros({8192}, at::TensorOptions().dtype(at::kInt).device(device))).first;
+  }
+  return it->second.data_ptr<int>();
+}
+
 // LRU cache of tensor maps keyed by (base, rows, cols, stride, box_rows).
 struct MapKey {
   uintptr_t base;
@@ -137,7 +150,7 @@ Tensor rope_store(Tensor qkv, Tensor positions, Tensor cos, Tensor sin, int64_t 
 }
 
 Tensor attention(Tensor q, Tensor k_cache, Tensor v_cache, Tensor kv_len, Tensor n_new, c10::optional<Tensor> mask,
-                 double scale, int64_t q_offset) {
+                 double scale, int64_t q_offset, c10::optional<Tensor> trace) {
   CHECK_CUDA(q);
   CHECK_BF16(q);
   CHECK_BF16(k_cache);
@@ -170,7 +183,10 @@ Tensor attention(Tensor q, Tensor k_cache, Tensor v_cache, Tensor kv_len, Tensor
                                        plan.ws_floats > 0 ? ws.data_ptr<float>() : nullptr, kv_len.data_ptr<int>(),
                                        n_new.data_ptr<int>(), mask_ptr, B, T, H, Hkv, D, S,
                                        static_cast<float>(scale), static_cast<int>(q_offset), plan,
-                                       status_word(q.device()), at::cuda::getCurrentCUDAStream());
+                                       status_word(q.device()), at::cuda::getCurrentCUDAStream(),
+                                       trace.has_value() ? reinterpret_cast<unsigned long long*>(
+                                                               trace->data_ptr<int64_t>())
+                                                         : nullptr);
   TORCH_CHECK(rc == 0, "attention: unsupported shape (head_dim must be 128, H divisible by H_kv)");
   return out;
 }
@@ -207,8 +223,10 @@ Tensor linear(Tensor x, Tensor w) {
   if (splits > 1) ws = at::empty({static_cast<int64_t>(splits) * M * N}, x.options().dtype(at::kFloat));
   const CUtensorMap* tw = tensor_map(w.data_ptr(), N, K, K, 128);
   const CUtensorMap* tx = tensor_map(x.data_ptr(), M, K, K, bn);
+  cudaStream_t stream = at::cuda::getCurrentCUDAStream();
   const int rc = ecz::launch_gemm_bf16(tw, tx, y.data_ptr(), splits > 1 ? ws.data_ptr<float>() : nullptr, M, N, K,
-                                       splits, status_word(x.device()), at::cuda::getCurrentCUDAStream());
+                                       splits, status_word(x.device()), stream,
+                                       splits > 1 ? split_counters(x.device(), stream) : nullptr);
   TORCH_CHECK(rc == 0, "linear: K must be a multiple of 8 and N of 4");
   return y;
 }
@@ -221,7 +239,10 @@ Tensor argmax(Tensor x) {
   const int V = static_cast<int>(x.size(-1));
   const int rows = static_cast<int>(x.numel() / V);
   auto out = at::empty({rows}, x.options().dtype(at::kLong));
-  ecz::launch_argmax(x.data_ptr(), x.scalar_type() == at::kBFloat16, out.data_ptr<int64_t>(), rows, V,
+  const int slices = ecz::argmax_slices(rows, V);
+  auto part = at::empty({2 * static_cast<int64_t>(rows) * slices}, x.options().dtype(at::kFloat));
+  ecz::launch_argmax(x.data_ptr(), x.scalar_type() == at::kBFloat16, out.data_ptr<int64_t>(),
+                     part.data_ptr<float>(), reinterpret_cast<int*>(part.data_ptr<float>() + rows * slices), rows, V,
                      at::cuda::getCurrentCUDAStream());
   return out;
 }
@@ -290,7 +311,9 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.doc() = "economize_b200 sm_100a kernels (tcgen05 / TMA)";
   m.def("rmsnorm", &rmsnorm, "fused residual add + RMSNorm");
   m.def("rope_store", &rope_store, "rotary embedding + KV-cache write (+ optional QK-norm)");
-  m.def("attention", &attention, "tree-masked / causal attention over the slot cache (tcgen05)");
+  m.def("attention", &attention, "tree-masked / causal attention over the slot cache (tcgen05)",
+        py::arg("q"), py::arg("k_cache"), py::arg("v_cache"), py::arg("kv_len"), py::arg("n_new"), py::arg("mask"),
+        py::arg("scale"), py::arg("q_offset"), py::arg("trace") = py::none());
   m.def("silu_mul", &silu_mul, "SwiGLU activation of [gate; up]");
   m.def("linear", &linear, "x @ w.T on tcgen05 (swap-AB, split-K)");
   m.def("argmax", &argmax, "row argmax");

@@ -21,6 +21,8 @@ template <int kMaxVec>
 __global__ void __launch_bounds__(256) rmsnorm_kernel(const bf16* __restrict__ x, const bf16* __restrict__ resid,
                                                       const bf16* __restrict__ w, bf16* __restrict__ out,
                                                       bf16* __restrict__ resid_out, int hidden, float eps) {
+  pdl_trigger();
+  pdl_wait();
   const int row = blockIdx.x;
   const int nvec = hidden / 8;
   const uint4* xv = reinterpret_cast<const uint4*>(x + static_cast<size_t>(row) * hidden);
@@ -88,9 +90,9 @@ int launch_rmsnorm(const void* x, const void* resid, const void* w, void* out, v
   int threads = nvec < 256 ? ((nvec + 31) / 32) * 32 : 256;
   const int per = (nvec + threads - 1) / threads;
   auto args = [&](auto kernel) {
-    kernel<<<rows, threads, 0, stream>>>(static_cast<const bf16*>(x), static_cast<const bf16*>(resid),
-                                         static_cast<const bf16*>(w), static_cast<bf16*>(out),
-                                         static_cast<bf16*>(resid_out), hidden, eps);
+    launch_pdl(kernel, dim3(rows), dim3(threads), 0, stream, static_cast<const bf16*>(x),
+               static_cast<const bf16*>(resid), static_cast<const bf16*>(w), static_cast<bf16*>(out),
+               static_cast<bf16*>(resid_out), hidden, eps);
   };
   if (per <= 1) args(rmsnorm_kernel<1>);
   else if (per <= 2) args(rmsnorm_kernel<2>);
@@ -111,6 +113,8 @@ __global__ void __launch_bounds__(256) rope_store_kernel(
     bf16* __restrict__ v_cache, const int* __restrict__ kv_len, const int* __restrict__ n_new,
     const bf16* __restrict__ q_norm, const bf16* __restrict__ k_norm, float eps, int tokens, int T, int H, int Hkv,
     int S, int q_offset) {
+  pdl_trigger();
+  pdl_wait();
   constexpr int D = 128;
   const int warp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
   const int lane = threadIdx.x & 31;
@@ -173,10 +177,10 @@ int launch_rope_store(const void* qkv, const int* positions, const float* cos_t,
   if (D != 128) return -1;
   const long warps = static_cast<long>(B) * T * (H + Hkv);
   const int blocks = static_cast<int>((warps * 32 + 255) / 256);
-  rope_store_kernel<<<blocks, 256, 0, stream>>>(
-      static_cast<const bf16*>(qkv), positions, cos_t, sin_t, static_cast<bf16*>(q_out),
-      static_cast<bf16*>(k_cache), static_cast<bf16*>(v_cache), kv_len, n_new, static_cast<const bf16*>(q_norm),
-      static_cast<const bf16*>(k_norm), eps, B * T, T, H, Hkv, S, q_offset);
+  launch_pdl(rope_store_kernel, dim3(blocks), dim3(256), 0, stream, static_cast<const bf16*>(qkv), positions, cos_t,
+             sin_t, static_cast<bf16*>(q_out), static_cast<bf16*>(k_cache), static_cast<bf16*>(v_cache), kv_len,
+             n_new, static_cast<const bf16*>(q_norm), static_cast<const bf16*>(k_norm), eps, B * T, T, H, Hkv, S,
+             q_offset);
   return 0;
 }
 
@@ -185,6 +189,8 @@ int launch_rope_store(const void* qkv, const int* positions, const float* cos_t,
 // ---------------------------------------------------------------------------------------------------------------
 __global__ void __launch_bounds__(256) silu_mul_kernel(const bf16* __restrict__ gu, bf16* __restrict__ out,
                                                        int rows, int F) {
+  pdl_trigger();
+  pdl_wait();
   const long total = static_cast<long>(rows) * (F / 8);
   for (long i = blockIdx.x * static_cast<long>(blockDim.x) + threadIdx.x; i < total;
        i += static_cast<long>(gridDim.x) * blockDim.x) {
@@ -210,7 +216,8 @@ int launch_silu_mul(const void* gu, void* out, int rows, int F, cudaStream_t str
   const long total = static_cast<long>(rows) * (F / 8);
   int blocks = static_cast<int>(std::min<long>((total + 255) / 256, 148L * 16));
   if (blocks < 1) blocks = 1;
-  silu_mul_kernel<<<blocks, 256, 0, stream>>>(static_cast<const bf16*>(gu), static_cast<bf16*>(out), rows, F);
+  launch_pdl(silu_mul_kernel, dim3(blocks), dim3(256), 0, stream, static_cast<const bf16*>(gu),
+             static_cast<bf16*>(out), rows, F);
   return 0;
 }
 
@@ -224,23 +231,18 @@ __device__ __forceinline__ float to_f<bf16>(bf16 v) { return __bfloat162float(v)
 template <>
 __device__ __forceinline__ float to_f<float>(float v) { return v; }
 
-template <typename T>
-__global__ void __launch_bounds__(512) argmax_kernel(const T* __restrict__ x, int64_t* __restrict__ out, int V) {
-  const T* row = x + static_cast<size_t>(blockIdx.x) * V;
-  float best = -INFINITY;
-  int idx = 0x7fffffff;
-  for (int i = threadIdx.x; i < V; i += blockDim.x) {
-    const float v = to_f<T>(row[i]);
-    if (v > best) { best = v; idx = i; }  // strided scan: the first hit per thread is its smallest index
-  }
+// Two stages: every CTA scans one slice of a row with 16-byte loads and writes its (max, first index); a second
+// kernel reduces the slices of each row. Ties resolve to the smallest index in both stages.
+__device__ __forceinline__ void argmax_merge(float& best, int& idx, float ob, int oi) {
+  if (ob > best || (ob == best && oi < idx)) { best = ob; idx = oi; }
+}
+
+__device__ __forceinline__ void block_argmax(float& best, int& idx) {
 #pragma unroll
-  for (int o = 16; o > 0; o >>= 1) {
-    const float ob = __shfl_xor_sync(0xffffffffu, best, o);
-    const int oi = __shfl_xor_sync(0xffffffffu, idx, o);
-    if (ob > best || (ob == best && oi < idx)) { best = ob; idx = oi; }
-  }
-  __shared__ float sb[16];
-  __shared__ int si[16];
+  for (int o = 16; o > 0; o >>= 1)
+    argmax_merge(best, idx, __shfl_xor_sync(0xffffffffu, best, o), __shfl_xor_sync(0xffffffffu, idx, o));
+  __shared__ float sb[32];
+  __shared__ int si[32];
   if ((threadIdx.x & 31) == 0) { sb[threadIdx.x >> 5] = best; si[threadIdx.x >> 5] = idx; }
   __syncthreads();
   if (threadIdx.x < 32) {
@@ -248,19 +250,76 @@ __global__ void __launch_bounds__(512) argmax_kernel(const T* __restrict__ x, in
     best = threadIdx.x < nw ? sb[threadIdx.x] : -INFINITY;
     idx = threadIdx.x < nw ? si[threadIdx.x] : 0x7fffffff;
 #pragma unroll
-    for (int o = 16; o > 0; o >>= 1) {
-      const float ob = __shfl_xor_sync(0xffffffffu, best, o);
-      const int oi = __shfl_xor_sync(0xffffffffu, idx, o);
-      if (ob > best || (ob == best && oi < idx)) { best = ob; idx = oi; }
-    }
-    if (threadIdx.x == 0) out[blockIdx.x] = idx == 0x7fffffff ? 0 : idx;
+    for (int o = 16; o > 0; o >>= 1)
+      argmax_merge(best, idx, __shfl_xor_sync(0xffffffffu, best, o), __shfl_xor_sync(0xffffffffu, idx, o));
   }
 }
 
-int launch_argmax(const void* x, bool is_bf16, int64_t* out, int rows, int V, cudaStream_t stream) {
+template <typename T>
+__global__ void __launch_bounds__(256) argmax_slice_kernel(const T* __restrict__ x, float* __restrict__ part_v,
+                                                           int* __restrict__ part_i, int V, int slice) {
+  pdl_trigger();
+  pdl_wait();
+  constexpr int kVec = 16 / sizeof(T);
+  const int row = blockIdx.y, s = blockIdx.x;
+  const T* base = x + static_cast<size_t>(row) * V;
+  const int lo = s * slice, hi = min(V, lo + slice);
+  float best = -INFINITY;
+  int idx = 0x7fffffff;
+  const bool aligned = (V % kVec == 0) && (lo % kVec == 0);
+  if (aligned) {
+    for (int v = lo / kVec + threadIdx.x; v < hi / kVec; v += blockDim.x) {
+      const uint4 raw = reinterpret_cast<const uint4*>(base)[v];
+      const T* e = reinterpret_cast<const T*>(&raw);
+#pragma unroll
+      for (int j = 0; j < kVec; ++j) argmax_merge(best, idx, to_f<T>(e[j]), v * kVec + j);
+    }
+  } else {
+    for (int i = lo + threadIdx.x; i < hi; i += blockDim.x) argmax_merge(best, idx, to_f<T>(base[i]), i);
+  }
+  block_argmax(best, idx);
+  if (threadIdx.x == 0) {
+    part_v[row * gridDim.x + s] = best;
+    part_i[row * gridDim.x + s] = idx;
+  }
+}
+
+__global__ void __launch_bounds__(32) argmax_finish_kernel(const float* __restrict__ part_v,
+                                                           const int* __restrict__ part_i, int64_t* __restrict__ out,
+                                                           int slices) {
+  pdl_trigger();
+  pdl_wait();
+  const int row = blockIdx.x;
+  float best = -INFINITY;
+  int idx = 0x7fffffff;
+  for (int s = threadIdx.x; s < slices; s += 32) argmax_merge(best, idx, part_v[row * slices + s], part_i[row * slices + s]);
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1)
+    argmax_merge(best, idx, __shfl_xor_sync(0xffffffffu, best, o), __shfl_xor_sync(0xffffffffu, idx, o));
+  if (threadIdx.x == 0) out[row] = idx == 0x7fffffff ? 0 : idx;
+}
+
+int argmax_slices(int rows, int V) {
+  // enough CTAs to cover the SMs a few times, slices of at least 4096 entries
+  int slices = std::max(1, std::min((V + 4095) / 4096, (4 * 148 + rows - 1) / std::max(rows, 1)));
+  return std::min(slices, 32);
+}
+
+int launch_argmax(const void* x, bool is_bf16, int64_t* out, float* part_v, int* part_i, int rows, int V,
+                  cudaStream_t stream) {
   if (rows == 0) return 0;
-  if (is_bf16) argmax_kernel<bf16><<<rows, 512, 0, stream>>>(static_cast<const bf16*>(x), out, V);
-  else argmax_kernel<float><<<rows, 512, 0, stream>>>(static_cast<const float*>(x), out, V);
+  const int slices = argmax_slices(rows, V);
+  int slice = (V + slices - 1) / slices;
+  slice = (slice + 7) / 8 * 8;
+  dim3 grid(slices, rows);
+  if (is_bf16) {
+    launch_pdl(argmax_slice_kernel<bf16>, grid, dim3(256), 0, stream, static_cast<const bf16*>(x), part_v, part_i, V,
+               slice);
+  } else {
+    launch_pdl(argmax_slice_kernel<float>, grid, dim3(256), 0, stream, static_cast<const float*>(x), part_v, part_i,
+               V, slice);
+  }
+  launch_pdl(argmax_finish_kernel, dim3(rows), dim3(32), 0, stream, part_v, part_i, out, slices);
   return 0;
 }
 
@@ -273,6 +332,8 @@ int launch_argmax(const void* x, bool is_bf16, int64_t* out, int rows, int V, cu
 __global__ void greedy_accept_kernel(const int64_t* __restrict__ tokens, const int64_t* __restrict__ parents,
                                      const int64_t* __restrict__ pred, int* __restrict__ n_acc,
                                      int* __restrict__ path, int64_t* __restrict__ out, int T) {
+  pdl_trigger();
+  pdl_wait();
   const int b = blockIdx.x;
   const int lane = threadIdx.x;
   __shared__ int acc[64], depth[64], par[64];
@@ -308,7 +369,7 @@ __global__ void greedy_accept_kernel(const int64_t* __restrict__ tokens, const i
 int launch_greedy_accept(const int64_t* tokens, const int64_t* parents, const int64_t* pred, int* n_acc, int* path,
                          int64_t* out, int B, int T, cudaStream_t stream) {
   if (T > 64) return -1;
-  greedy_accept_kernel<<<B, 32, 0, stream>>>(tokens, parents, pred, n_acc, path, out, T);
+  launch_pdl(greedy_accept_kernel, dim3(B), dim3(32), 0, stream, tokens, parents, pred, n_acc, path, out, T);
   return 0;
 }
 
@@ -320,6 +381,8 @@ int launch_greedy_accept(const int64_t* tokens, const int64_t* parents, const in
 __global__ void kv_compact_kernel(bf16* __restrict__ cache, const int* __restrict__ kv_len,
                                   const int* __restrict__ path, const int* __restrict__ n_acc, int B, int Hkv, int S,
                                   int D, int T) {
+  pdl_trigger();
+  pdl_wait();
   const int lh = blockIdx.x;  // layer*2 + kv
   const int b = blockIdx.y, h = blockIdx.z;
   const int n = n_acc[b];
@@ -344,7 +407,8 @@ int launch_kv_compact(void* cache, const int* kv_len, const int* path, const int
   const int threads = max_depth * (D / 8);
   if (threads > 1024 || D % 8) return -1;
   dim3 grid(LH, B, Hkv);
-  kv_compact_kernel<<<grid, threads, 0, stream>>>(static_cast<bf16*>(cache), kv_len, path, n_acc, B, Hkv, S, D, T);
+  launch_pdl(kv_compact_kernel, grid, dim3(threads), 0, stream, static_cast<bf16*>(cache), kv_len, path, n_acc, B,
+             Hkv, S, D, T);
   return 0;
 }
 

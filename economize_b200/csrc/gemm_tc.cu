@@ -36,8 +36,8 @@ struct GemmCfg {
 template <int BN>
 __global__ void __launch_bounds__(128, 1)
     gemm_swapab_kernel(const __grid_constant__ CUtensorMap tm_w, const __grid_constant__ CUtensorMap tm_x,
-                       bf16* __restrict__ y, float* __restrict__ ws, int M, int N, int K, int kb_per_split,
-                       unsigned* status) {
+                       bf16* __restrict__ y, float* __restrict__ ws, int* __restrict__ counters, int M, int N,
+                       int K, int kb_per_split, unsigned* status) {
   using Cfg = GemmCfg<BN>;
   constexpr int S = Cfg::kStages;
   extern __shared__ uint8_t smem_raw[];
@@ -50,6 +50,7 @@ __global__ void __launch_bounds__(128, 1)
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(accum + 1);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
+  pdl_trigger();
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int n0 = blockIdx.x * kBM, m0 = blockIdx.y * BN, split = blockIdx.z;
   const int total_kb = (K + kBK - 1) / kBK;
@@ -76,10 +77,19 @@ __global__ void __launch_bounds__(128, 1)
 
   if (nkb > 0 && warp == 0 && lane == 0) {
     // ---- TMA producer ----
-    for (int kb = 0; kb < nkb; ++kb) {
+    // The weights do not depend on the previous kernel: the first ring of weight tiles is requested before
+    // griddepcontrol.wait, so it streams while the predecessor finishes; activations follow after the wait.
+    const int pre = nkb < S ? nkb : S;
+    for (int kb = 0; kb < pre; ++kb) {
+      mbar_arrive_expect_tx(&full[kb], Cfg::kStageBytes);
+      tma_load_2d(a_tiles + kb * kABytes, &tm_w, &full[kb], (kb0 + kb) * kBK, n0);
+    }
+    pdl_wait();
+    for (int kb = 0; kb < pre; ++kb) tma_load_2d(b_tiles + kb * Cfg::kBBytes, &tm_x, &full[kb], (kb0 + kb) * kBK, m0);
+    for (int kb = pre; kb < nkb; ++kb) {
       const int s = kb % S;
       const uint32_t use = kb / S;
-      if (kb >= S && !mbar_wait(&empty[s], (use & 1u) ^ 1u, status, kStatusWaitEmpty, abort_flag)) break;
+      if (!mbar_wait(&empty[s], (use & 1u) ^ 1u, status, kStatusWaitEmpty, abort_flag)) break;
       mbar_arrive_expect_tx(&full[s], Cfg::kStageBytes);
       const int kx = (kb0 + kb) * kBK;
       tma_load_2d(a_tiles + s * kABytes, &tm_w, &full[s], kx, n0);
@@ -108,6 +118,7 @@ __global__ void __launch_bounds__(128, 1)
 
   // ---- epilogue: warp w owns TMEM lanes 32w..32w+31 = output features n0 + 32w + lane ----
   if (nkb > 0) mbar_wait(accum, 0, status, kStatusWaitAccum, abort_flag);
+  pdl_wait();       // no global write before the predecessor grid has completed
   __syncthreads();  // a failed wait set abort_flag; the decision below is uniform across the CTA
   tc_fence_after();
   const bool ok = nkb > 0 && !*abort_flag;
@@ -139,10 +150,64 @@ __global__ void __launch_bounds__(128, 1)
   tc_fence_before();
   __syncthreads();
   if (warp == 0) tmem_dealloc(tmem, Cfg::kTmemCols);
+  if (ok && ws != nullptr && counters != nullptr) {
+    // In-kernel split-K reduction: the last CTA of this output tile (counted with a self-resetting atomic) sums
+    // the partials of all splits in split order, so the result does not depend on which CTA finishes last.
+    __shared__ int last;
+    __threadfence();
+    __syncthreads();
+    const int tile = blockIdx.y * gridDim.x + blockIdx.x;
+    if (threadIdx.x == 0) last = atomicAdd(&counters[tile], 1) == static_cast<int>(gridDim.z) - 1;
+    __syncthreads();
+    if (last) {
+      __threadfence();
+      // thread t sums 4 consecutive columns (group t % 32) of rows m0 + t / 32, + 4, + 8, ...; four rows' loads of
+      // every split are issued before they are summed, in split order
+      const int cg = threadIdx.x & 31, rp = threadIdx.x >> 5;
+      const int col = n0 + cg * 4;
+      const int nsplit = static_cast<int>(gridDim.z);
+      const int m_end = min(M, m0 + BN);
+      if (col < N) {
+        for (int mb = m0 + rp; mb < m_end; mb += 16) {
+          float4 acc[4];
+#pragma unroll
+          for (int u = 0; u < 4; ++u) acc[u] = make_float4(0.f, 0.f, 0.f, 0.f);
+          for (int sp = 0; sp < nsplit; ++sp) {
+            float4 v[4];
+#pragma unroll
+            for (int u = 0; u < 4; ++u) {
+              const int m = mb + 4 * u;
+              v[u] = m < m_end ? __ldcg(reinterpret_cast<const float4*>(ws + (static_cast<size_t>(sp) * M + m) * N + col))
+                               : make_float4(0.f, 0.f, 0.f, 0.f);
+            }
+#pragma unroll
+            for (int u = 0; u < 4; ++u) {
+              acc[u].x += v[u].x; acc[u].y += v[u].y; acc[u].z += v[u].z; acc[u].w += v[u].w;
+            }
+          }
+#pragma unroll
+          for (int u = 0; u < 4; ++u) {
+            const int m = mb + 4 * u;
+            if (m < m_end) {
+              __nv_bfloat162 lo = __floats2bfloat162_rn(acc[u].x, acc[u].y);
+              __nv_bfloat162 hi = __floats2bfloat162_rn(acc[u].z, acc[u].w);
+              uint2 packed;
+              packed.x = *reinterpret_cast<uint32_t*>(&lo);
+              packed.y = *reinterpret_cast<uint32_t*>(&hi);
+              *reinterpret_cast<uint2*>(y + static_cast<size_t>(m) * N + col) = packed;
+            }
+          }
+        }
+      }
+      if (threadIdx.x == 0) counters[tile] = 0;
+    }
+  }
 }
 
 __global__ void __launch_bounds__(256) splitk_reduce_kernel(const float* __restrict__ ws, bf16* __restrict__ y,
                                                              long total, int splits) {
+  pdl_trigger();
+  pdl_wait();
   for (long i = (blockIdx.x * static_cast<long>(blockDim.x) + threadIdx.x) * 4; i < total;
        i += static_cast<long>(gridDim.x) * blockDim.x * 4) {
     float4 acc = *reinterpret_cast<const float4*>(ws + i);
@@ -160,8 +225,8 @@ __global__ void __launch_bounds__(256) splitk_reduce_kernel(const float* __restr
 }
 
 template <int BN>
-int run_gemm(const CUtensorMap& tm_w, const CUtensorMap& tm_x, void* y, float* ws, int M, int N, int K,
-             int splits, unsigned* status, cudaStream_t stream) {
+int run_gemm(const CUtensorMap& tm_w, const CUtensorMap& tm_x, void* y, float* ws, int* counters, int M, int N,
+             int K, int splits, unsigned* status, cudaStream_t stream) {
   using Cfg = GemmCfg<BN>;
   static bool configured = false;
   if (!configured) {
@@ -172,12 +237,13 @@ int run_gemm(const CUtensorMap& tm_w, const CUtensorMap& tm_x, void* y, float* w
   const int kbps = (total_kb + splits - 1) / splits;
   splits = (total_kb + kbps - 1) / kbps;  // no empty split
   dim3 grid((N + kBM - 1) / kBM, (M + BN - 1) / BN, splits);
-  gemm_swapab_kernel<BN><<<grid, 128, Cfg::kSmem, stream>>>(tm_w, tm_x, static_cast<bf16*>(y),
-                                                            splits > 1 ? ws : nullptr, M, N, K, kbps, status);
-  if (splits > 1) {
+  launch_pdl(gemm_swapab_kernel<BN>, grid, dim3(128), Cfg::kSmem, stream, tm_w, tm_x, static_cast<bf16*>(y),
+             splits > 1 ? ws : nullptr, splits > 1 ? counters : nullptr, M, N, K, kbps, status);
+  if (splits > 1 && counters == nullptr) {
     const long total = static_cast<long>(M) * N;
     const int blocks = static_cast<int>(std::min<long>((total / 4 + 255) / 256, 148L * 8));
-    splitk_reduce_kernel<<<std::max(blocks, 1), 256, 0, stream>>>(ws, static_cast<bf16*>(y), total, splits);
+    launch_pdl(splitk_reduce_kernel, dim3(std::max(blocks, 1)), dim3(256), 0, stream,
+               static_cast<const float*>(ws), static_cast<bf16*>(y), total, splits);
   }
   return 0;
 }
@@ -206,13 +272,13 @@ int gemm_splits(int M, int N, int K, int num_sms) {
 }
 
 int launch_gemm_bf16(const CUtensorMap* tm_w, const CUtensorMap* tm_x, void* y, float* ws, int M, int N, int K,
-                     int splits, unsigned* status, cudaStream_t stream) {
+                     int splits, unsigned* status, cudaStream_t stream, int* counters) {
   if (K % 8 != 0 || N % 4 != 0) return -1;
   switch (gemm_block_n(M)) {
-    case 32: return run_gemm<32>(*tm_w, *tm_x, y, ws, M, N, K, splits, status, stream);
-    case 64: return run_gemm<64>(*tm_w, *tm_x, y, ws, M, N, K, splits, status, stream);
-    case 128: return run_gemm<128>(*tm_w, *tm_x, y, ws, M, N, K, splits, status, stream);
-    default: return run_gemm<256>(*tm_w, *tm_x, y, ws, M, N, K, splits, status, stream);
+    case 32: return run_gemm<32>(*tm_w, *tm_x, y, ws, counters, M, N, K, splits, status, stream);
+    case 64: return run_gemm<64>(*tm_w, *tm_x, y, ws, counters, M, N, K, splits, status, stream);
+    case 128: return run_gemm<128>(*tm_w, *tm_x, y, ws, counters, M, N, K, splits, status, stream);
+    default: return run_gemm<256>(*tm_w, *tm_x, y, ws, counters, M, N, K, splits, status, stream);
   }
 }
 

@@ -22,7 +22,9 @@ int launch_rope_store(const void* qkv, const int* positions, const float* cos_t,
                       const void* k_norm, float eps, int B, int T, int H, int Hkv, int D, int S, int q_offset,
                       cudaStream_t stream);
 int launch_silu_mul(const void* gu, void* out, int rows, int F, cudaStream_t stream);
-int launch_argmax(const void* x, bool is_bf16, int64_t* out, int rows, int V, cudaStream_t stream);
+int argmax_slices(int rows, int V);
+int launch_argmax(const void* x, bool is_bf16, int64_t* out, float* part_v, int* part_i, int rows, int V,
+                  cudaStream_t stream);
 int launch_greedy_accept(const int64_t* tokens, const int64_t* parents, const int64_t* pred, int* n_acc, int* path,
                          int64_t* out, int B, int T, cudaStream_t stream);
 int launch_kv_compact(void* cache, const int* kv_len, const int* path, const int* n_acc, int LH, int B, int Hkv,
@@ -31,14 +33,17 @@ int launch_kv_compact(void* cache, const int* kv_len, const int* path, const int
 // gemm_tc.cu
 int gemm_block_n(int M);
 int gemm_splits(int M, int N, int K, int num_sms);
+// With `counters` (a zeroed int array of at least num_sms entries, private to the stream) the split-K partials are
+// reduced inside the GEMM by the last CTA of each tile; without, by a second kernel.
 int launch_gemm_bf16(const CUtensorMap* tm_w, const CUtensorMap* tm_x, void* y, float* ws, int M, int N, int K,
-                     int splits, unsigned* status, cudaStream_t stream);
+                     int splits, unsigned* status, cudaStream_t stream, int* counters = nullptr);
 
 // attention.cu
 AttnPlan attention_plan(int B, int T, int H, int Hkv, int S, int num_sms);
 int launch_attention(const void* q, const CUtensorMap* tm_k, const CUtensorMap* tm_v, void* out, float* ws,
                      const int* kv_len, const int* n_new, const int64_t* mask, int B, int T, int H, int Hkv, int D,
-                     int S, float scale, int q_offset, const AttnPlan& plan, unsigned* status, cudaStream_t stream);
+                     int S, float scale, int q_offset, const AttnPlan& plan, unsigned* status, cudaStream_t stream,
+                     unsigned long long* trace = nullptr);
 
 // tmap.cpp: a 2-D bf16 tensor map over a row-major [rows, cols] matrix with a {64, box_rows} box and the 128-byte
 // swizzle (cols * 2 bytes must be a multiple of 16). Returns 0 on success.

@@ -3,11 +3,21 @@
 #include <cuda.h>
 #include <cuda_runtime.h>
 
+#include <cstdlib>
 #include <mutex>
 
 #include "launchers.h"
 
 namespace ecz {
+
+// Programmatic dependent launch is on unless ECZ_PDL=0.
+bool pdl_enabled() {
+  static const bool on = [] {
+    const char* v = std::getenv("ECZ_PDL");
+    return v == nullptr || v[0] != '0';
+  }();
+  return on;
+}
 
 namespace {
 using EncodeFn = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,

@@ -29,7 +29,7 @@ from ..models.llama import CausalLM
 from ..runtime.cache import KVCache, StepBatch
 from .config import DecodeConfig
 from .drafter import DraftModel
-from .tree import LOGP_FLOOR, TreeOptions, ancestor_bits, chain_parents, popcount64, select_candidates
+from .tree import LOGP_FLOOR, TreeOptions, ancestor_bits, popcount64, select_candidates
 
 __all__ = ["DecodeResult", "GenerationStats", "SpecEngine"]
 
@@ -377,7 +377,8 @@ class SpecEngine:
             tok = drafter.to_target(ops.argmax(logits[:, 0]))
             state = out
             tokens.append(tok)
-        return torch.stack(tokens, 1), chain_parents(batch, k, dev) - 0
+        parents = (torch.arange(k, device=dev) - 1).expand(batch, k).contiguous()  # -1: child of the root
+        return torch.stack(tokens, 1), parents
 
     def _draft_tree(self, st: _State) -> tuple[torch.Tensor, torch.Tensor]:
         drafter, tree = self.drafter, self.tree

@@ -64,13 +64,34 @@ class Eagle3Technique(Technique):
         self.reset_parameters()
 
     @torch.no_grad()
-    def reset_parameters(self, seed: int | None = None, std: float = 0.02) -> None:
+    def reset_parameters(self, seed: int | None = None, std: float = 0.02, identity: bool = False) -> None:
+        """Random N(0, std) matrices. With ``identity``, start as an early exit of the target instead: ``fc``
+        selects the highest fused feature, and the attention and MLP output maps are zero, so the draft layer
+        passes that feature through and the (target-initialised) head drafts what the target's head would say on
+        it; training then learns the corrections."""
         gen = None
         if seed is not None:
             gen = torch.Generator(device=self.fc.device)
             gen.manual_seed(seed)
         for p in (self.fc, self.layer.wqkv, self.layer.wo, self.layer.w_gate_up, self.layer.w_down):
             p.copy_(torch.randn(p.shape, generator=gen, device=p.device, dtype=torch.float32) * std)
+        if identity:
+            h = self.fc.shape[0]
+            self.fc.zero_()
+            self.fc[:, -h:].copy_(torch.eye(h, device=self.fc.device, dtype=self.fc.dtype))
+            self.layer.wo.zero_()
+            self.layer.w_down.zero_()
+
+    @torch.no_grad()
+    def draft_vocab_from(self, tokens: torch.Tensor) -> torch.Tensor:
+        """Choose the draft vocabulary as the ``draft_vocab`` most frequent ids of ``tokens`` (EAGLE-3's rule;
+        ties and unseen ids fill up in id order) and return the chosen ids."""
+        vocab = self.t2d.numel()
+        counts = torch.bincount(tokens.reshape(-1).long().to(self.d2t.device), minlength=vocab)[:vocab].float()
+        order = torch.argsort(-counts - torch.arange(vocab, device=counts.device) * 1e-9 / vocab)
+        ids = order[: self.draft_vocab]
+        self.set_draft_vocab(ids)
+        return ids
 
     @torch.no_grad()
     def set_draft_vocab(self, token_ids: torch.Tensor) -> None:

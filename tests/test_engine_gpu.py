@@ -68,3 +68,14 @@ def test_graph_replay_matches_eager(em, cuda):
     for a, b in zip(eager, graphed):
         assert torch.equal(a.tokens, b.tokens)
         assert a.accepted == b.accepted
+
+
+def test_chain_is_bit_identical_to_plain(em, cuda):
+    """A verified chain occupies the same cache slots as plain decoding and every kernel reduces a row the same
+    way whatever the number of rows in the pass, so greedy chain speculation reproduces plain decoding exactly."""
+    prompts = _prompts(cuda)
+    plain = em.decode_batch(prompts, 48, decoding=eco.DecodeConfig(cycle_length=1))
+    for graphs in (False, True):
+        chain = em.decode_batch(prompts, 48, decoding=eco.DecodeConfig(cycle_length=5, cuda_graphs=graphs))
+        for p, c in zip(plain, chain):
+            assert torch.equal(p.tokens, c.tokens)
