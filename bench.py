@@ -43,7 +43,8 @@ def parse() -> argparse.Namespace:
     p.add_argument("--batch", type=int, default=1)
     p.add_argument("--prompt-len", type=int, default=512)
     p.add_argument("--new-tokens", type=int, default=256)
-    p.add_argument("--train-steps", type=int, default=100)
+    p.add_argument("--train-steps", type=int, default=150)
+    p.add_argument("--train-rounds", type=int, default=3)
     p.add_argument("--impl", choices=("ours", "reference"), default="ours")
     p.add_argument("--model", choices=("llama31_8b", "tiny"), default="llama31_8b")
     p.add_argument("--no-graphs", action="store_true")
@@ -147,7 +148,8 @@ CACHE_DIR = os.environ.get("ECZ_BENCH_CACHE", "/tmp/economize_b200_bench")
 
 
 def _cache_path(args, rank: int, world: int) -> str:
-    key = f"{args.model}-b{args.batch}-p{args.prompt_len}-n{args.new_tokens}-t{args.train_steps}-r{rank}-w{world}-v2"
+    key = (f"{args.model}-b{args.batch}-p{args.prompt_len}-n{args.new_tokens}-t{args.train_steps}x{args.train_rounds}"
+           f"-r{rank}-w{world}-v4")
     return os.path.join(CACHE_DIR, f"drafter-{key}.pt")
 
 
@@ -210,21 +212,57 @@ def build_drafter(target, args, rank: int, world: int, prompts, hf=None):
     if args.train_steps > 0:
         from economize_b200.train import fit
 
+        def with_prompts(results):
+            return torch.stack([torch.cat([p, r.tokens.to(p.device)]) for p, r in zip(prompts, results)])
+
         plain = em.decode_batch(list(prompts), args.new_tokens,
                                 decoding=eco.DecodeConfig(cycle_length=1, cuda_graphs=True))
-        rows = [torch.stack([torch.cat([p, r.tokens.to(p.device)]) for p, r in zip(prompts, plain)])]
+        data = with_prompts(plain)
         ref = reference_module()
+        ref_model = None
+        own_hf = False
         if ref is not None:
             own_hf = hf is None
             hf = hf if hf is not None else hf_twin(target)
-            rows.append(plain_continuations_ref(ref, hf, prompts, args.new_tokens))
-            if own_hf:
-                del hf
-                torch.cuda.empty_cache()
-        data = torch.cat(rows)
+            try:
+                from economize.techniques.eagle3 import Eagle3Config as RefEagle3Config
+
+                ref_model = ref.apply(hf, RefEagle3Config(draft_vocab=vocab, param_dtype="model"))
+                ref_cfg = ref.DecodeConfig(cycle_length=TREE["depth"] + 1, draft_policy="dynamic_tree",
+                                           draft_policy_options=dict(TREE), cuda_graphs=True)
+            except Exception as err:
+                print(f"[bench] reference drafter unavailable for training rows ({err})", file=sys.stderr)
+
+        def ref_trajectories():
+            ref_tech = ref_model.techniques["eagle3"]
+            cur = ref_tech.state_dict()
+            ref_tech.load_state_dict({k: v.to(cur[k].device, cur[k].dtype)
+                                      for k, v in to_reference_state(tech).items()})
+            return with_prompts(ref_model.decode_batch(list(prompts), args.new_tokens, decoding=ref_cfg))
+
         tech.draft_vocab_from(data[:, args.prompt_len:])
-        fit(em, data, steps=args.train_steps, batch_size=min(4, data.shape[0]), seed=0, lr=1e-3, warmup_steps=5,
-            log_every=max(1, args.train_steps))
+        if ref_model is not None:  # the reference's own greedy trajectory (its tree path, untrained drafter)
+            data = torch.cat([data, ref_trajectories()])
+            tech.extend_draft_vocab(data[:, args.prompt_len:], data[:1, args.prompt_len:])
+        # bf16 tree verification rounds differently from one-token passes and the random target is chaotic, so
+        # every implementation's speculative trajectory drifts from its plain one; each round adds the
+        # trajectories the current drafter produces in both implementations.
+        rounds = max(1, args.train_rounds)
+        for rnd in range(rounds):
+            fit(em, data, steps=max(1, args.train_steps // rounds), batch_size=min(4, data.shape[0]), seed=rnd,
+                lr=1e-3, warmup_steps=5, log_every=max(1, args.train_steps))
+            if rnd + 1 < rounds:
+                seen = data[:, args.prompt_len:]
+                new = [with_prompts(em.decode_batch(list(prompts), args.new_tokens, decoding=decode_config(args)))]
+                if ref_model is not None:
+                    new.append(ref_trajectories())
+                data = torch.cat([data, *new])
+                tech.extend_draft_vocab(data[:, args.prompt_len:], seen)
+        if ref_model is not None:
+            ref_model.detach()
+        if own_hf:
+            del hf
+            torch.cuda.empty_cache()
     state = to_reference_state(tech)
     os.makedirs(CACHE_DIR, exist_ok=True)
     tmp = path + f".{os.getpid()}.tmp"
@@ -388,8 +426,9 @@ def main() -> None:
             "mean_accepted_len": round(tau, 4) if tau is not None else None,
             "config": {"model": "Llama-3.1-8B arch" if args.model == "llama31_8b" else "tiny",
                        "drafter": "EAGLE-3 (draft vocab 32000), dynamic tree depth 6 topk 10 nodes 60; trained "
-                                  f"{args.train_steps} steps on both implementations' plain greedy continuations of "
-                                  "the benchmark prompts (same weights in both arms)",
+                                  f"{args.train_steps} steps in {args.train_rounds} rounds on the greedy and "
+                                  "speculative trajectories of both implementations on the benchmark prompts (same "
+                                  "weights in both arms)",
                        "global_batch": args.batch * world, "seq_len": args.prompt_len,
                        "new_tokens": args.new_tokens, "parallelism": f"dp{world}",
                        "train_steps": args.train_steps, "cuda_graphs": not args.no_graphs,

@@ -218,15 +218,26 @@ Tensor linear(Tensor x, Tensor w) {
   auto y = at::empty({M, N}, x.options());
   if (M == 0) return y;
   const int bn = ecz::gemm_block_n(M);
-  const int splits = ecz::gemm_splits(M, N, K, num_sms(x.get_device()));
-  Tensor ws;
-  if (splits > 1) ws = at::empty({static_cast<int64_t>(splits) * M * N}, x.options().dtype(at::kFloat));
+  const int sms = num_sms(x.get_device());
+  const long tiles = static_cast<long>((N + 127) / 128) * ((M + bn - 1) / bn);
   const CUtensorMap* tw = tensor_map(w.data_ptr(), N, K, K, 128);
   const CUtensorMap* tx = tensor_map(x.data_ptr(), M, K, K, bn);
   cudaStream_t stream = at::cuda::getCurrentCUDAStream();
-  const int rc = ecz::launch_gemm_bf16(tw, tx, y.data_ptr(), splits > 1 ? ws.data_ptr<float>() : nullptr, M, N, K,
-                                       splits, status_word(x.device()), stream,
-                                       splits > 1 ? split_counters(x.device(), stream) : nullptr);
+  int rc;
+  if (tiles >= sms) {
+    // enough tiles for every SM: persistent stream-K balances the last wave
+    auto ws = at::empty({ecz::gemm_persistent_ws_floats(M, N, K, sms)}, x.options().dtype(at::kFloat));
+    rc = ecz::launch_gemm_persistent(tw, tx, y.data_ptr(), ws.data_ptr<float>(), split_counters(x.device(), stream),
+                                     M, N, K, sms, status_word(x.device()), stream);
+  } else {
+    // fewer tiles than SMs: split K evenly, reduced inside the kernel by each tile's last CTA
+    const int splits = ecz::gemm_splits(M, N, K, sms);
+    Tensor ws;
+    if (splits > 1) ws = at::empty({static_cast<int64_t>(splits) * M * N}, x.options().dtype(at::kFloat));
+    rc = ecz::launch_gemm_bf16(tw, tx, y.data_ptr(), splits > 1 ? ws.data_ptr<float>() : nullptr, M, N, K, splits,
+                               status_word(x.device()), stream,
+                               splits > 1 ? split_counters(x.device(), stream) : nullptr);
+  }
   TORCH_CHECK(rc == 0, "linear: K must be a multiple of 8 and N of 4");
   return y;
 }

@@ -248,6 +248,242 @@ int run_gemm(const CUtensorMap& tm_w, const CUtensorMap& tm_x, void* y, float* w
   return 0;
 }
 
+// ---------------------------------------------------------------------------------------------------------------
+// Persistent stream-K GEMM (the main path)
+// ---------------------------------------------------------------------------------------------------------------
+// Work = tiles x K-blocks "units" (tile-major). CTA c of C owns units [c*U/C, (c+1)*U/C); each maximal run of its
+// units inside one tile is a segment. Warp 0 streams (W, X) stages, warp 1 issues UMMAs into one of two TMEM
+// accumulators, warps 2-5 drain the other. A segment that covers its whole tile is written as bf16 directly;
+// otherwise its fp32 partial goes to slot 2c (first tile of the CTA) or 2c+1 (last tile), and the tile's last
+// contributor (counted on counters[c_lo]) sums the contributors' partials in CTA order.
+struct StreamK {
+  int units, ctas, kb, n_tiles;
+  __device__ __forceinline__ int start(int c) const { return static_cast<int>((static_cast<long long>(c) * units) / ctas); }
+  __device__ __forceinline__ int cta_of(int u) const {
+    return static_cast<int>(((static_cast<long long>(u) + 1) * ctas + units - 1) / units) - 1;
+  }
+};
+
+template <int BN>
+__global__ void __launch_bounds__(192, 1)
+    gemm_persistent_kernel(const __grid_constant__ CUtensorMap tm_w, const __grid_constant__ CUtensorMap tm_x,
+                           bf16* __restrict__ y, float* __restrict__ ws, int* __restrict__ counters, int M, int N,
+                           int K, unsigned* status) {
+  using Cfg = GemmCfg<BN>;
+  constexpr int S = Cfg::kStages;
+  constexpr int kAccCols = BN;
+  constexpr uint32_t kTmemCols = 2 * BN < 32 ? 32 : 2 * BN;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* a_tiles = smem;
+  uint8_t* b_tiles = smem + S * kABytes;
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + S * Cfg::kStageBytes);
+  uint64_t* empty = full + S;
+  uint64_t* acc_full = empty + S;   // [2]
+  uint64_t* acc_empty = acc_full + 2;  // [2]
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(acc_empty + 2);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+  int* last_flag = const_cast<int*>(reinterpret_cast<volatile int*>(tmem_slot + 2));
+
+  pdl_trigger();
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int n_tiles = (N + kBM - 1) / kBM;
+  const int m_tiles = (M + BN - 1) / BN;
+  StreamK sk;
+  sk.kb = (K + kBK - 1) / kBK;
+  sk.units = n_tiles * m_tiles * sk.kb;
+  sk.ctas = gridDim.x;
+  sk.n_tiles = n_tiles;
+  const int c = blockIdx.x;
+  const int u_begin = sk.start(c), u_end = sk.start(c + 1);
+
+  if (threadIdx.x == 0) {
+    for (int i = 0; i < S; ++i) {
+      mbar_init(&full[i], 1);
+      mbar_init(&empty[i], 1);
+    }
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&acc_full[i], 1);
+      mbar_init(&acc_empty[i], 4);
+    }
+    *abort_flag = 0;
+    fence_mbar_init();
+    tma_prefetch_desc(&tm_w);
+    tma_prefetch_desc(&tm_x);
+  }
+  __syncwarp();
+  if (warp == 0) tmem_alloc(tmem_slot, kTmemCols);
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+
+  if (warp == 0 && lane == 0) {
+    // ---- TMA producer: walks every unit of this CTA in order ----
+    const int n_units = u_end - u_begin;
+    const int pre = n_units < S ? n_units : S;
+    for (int g = 0; g < pre; ++g) {  // weight tiles of the first ring before waiting on the predecessor
+      const int u = u_begin + g, t = u / sk.kb, kb = u % sk.kb;
+      mbar_arrive_expect_tx(&full[g], Cfg::kStageBytes);
+      tma_load_2d(a_tiles + g * kABytes, &tm_w, &full[g], kb * kBK, (t % n_tiles) * kBM);
+    }
+    pdl_wait();
+    for (int g = 0; g < pre; ++g) {
+      const int u = u_begin + g, t = u / sk.kb, kb = u % sk.kb;
+      tma_load_2d(b_tiles + g * Cfg::kBBytes, &tm_x, &full[g], kb * kBK, (t / n_tiles) * BN);
+    }
+    for (int g = pre; g < n_units; ++g) {
+      const int st = g % S;
+      const uint32_t use = g / S;
+      if (!mbar_wait(&empty[st], (use & 1u) ^ 1u, status, kStatusWaitEmpty, abort_flag)) break;
+      const int u = u_begin + g, t = u / sk.kb, kb = u % sk.kb;
+      mbar_arrive_expect_tx(&full[st], Cfg::kStageBytes);
+      tma_load_2d(a_tiles + st * kABytes, &tm_w, &full[st], kb * kBK, (t % n_tiles) * kBM);
+      tma_load_2d(b_tiles + st * Cfg::kBBytes, &tm_x, &full[st], kb * kBK, (t / n_tiles) * BN);
+    }
+  } else if (warp == 1 && lane == 0) {
+    // ---- MMA issuer ----
+    constexpr uint32_t idesc = idesc_bf16_f32(kBM, BN);
+    int g = 0, seg = 0;
+    bool good = true;
+    for (int u = u_begin; u < u_end && good; ++seg) {
+      const int t = u / sk.kb;
+      const int seg_end = min(u_end, (t + 1) * sk.kb);
+      const int buf = seg & 1;
+      if (!mbar_wait(&acc_empty[buf], ((seg >> 1) & 1) ^ 1, status, kStatusWaitAccum, abort_flag)) break;
+      tc_fence_after();
+      const uint32_t acc = tmem + buf * kAccCols;
+      const int seg_start = u;
+      for (; u < seg_end; ++u, ++g) {
+        const int st = g % S;
+        if (!mbar_wait(&full[st], (g / S) & 1u, status, kStatusWaitFull, abort_flag)) { good = false; break; }
+        tc_fence_after();
+        const uint32_t a_addr = smem_u32(a_tiles + st * kABytes);
+        const uint32_t b_addr = smem_u32(b_tiles + st * Cfg::kBBytes);
+        const bool first = u == seg_start;
+#pragma unroll
+        for (int kk = 0; kk < kBK / 16; ++kk) {
+          umma_bf16(acc, desc_kmajor_sw128(a_addr + kk * 32), desc_kmajor_sw128(b_addr + kk * 32), idesc,
+                    (first && kk == 0) ? 0u : 1u);
+        }
+        umma_commit(&empty[st]);
+      }
+      umma_commit(&acc_full[buf]);  // also after a failure, so the epilogue's wait ends
+    }
+  } else if (warp >= 2) {
+    // ---- epilogue: warp w drains TMEM lanes 32 * (w % 4) .. (output features) ----
+    const int quad = warp & 3;
+    const uint32_t lane_base = static_cast<uint32_t>(quad * 32) << 16;
+    const int et = threadIdx.x - 64;  // 0..127
+    pdl_wait();  // no global write before the predecessor grid completed
+    int seg = 0;
+    for (int u = u_begin; u < u_end; ++seg) {
+      const int t = u / sk.kb;
+      const int seg_begin = u;
+      const int seg_end = min(u_end, (t + 1) * sk.kb);
+      u = seg_end;
+      const int buf = seg & 1;
+      mbar_wait(&acc_full[buf], (seg >> 1) & 1, status, kStatusWaitAccum, abort_flag);  // sets abort_flag on failure
+      asm volatile("bar.sync 1, 128;" ::: "memory");  // the decision below is uniform over the epilogue warps
+      tc_fence_after();
+      const int n0 = (t % n_tiles) * kBM, m0 = (t / n_tiles) * BN;
+      const int n = n0 + quad * 32 + lane;
+      const bool whole = seg_begin == t * sk.kb && seg_end == (t + 1) * sk.kb;
+      const bool live = !*abort_flag;
+      float* part = nullptr;
+      if (!whole) part = ws + (static_cast<size_t>(2 * c + (t == u_begin / sk.kb ? 0 : 1)) * BN) * kBM;
+      const uint32_t acc = tmem + buf * kAccCols;
+#pragma unroll 1
+      for (int cc = 0; cc < BN; cc += 16) {
+        float v[16];
+        tmem_ld16(acc + lane_base + cc, v);
+        if (!live) continue;
+        if (whole) {
+          if (n < N) {
+#pragma unroll
+            for (int j = 0; j < 16; ++j) {
+              const int m = m0 + cc + j;
+              if (m < M) y[static_cast<size_t>(m) * N + n] = __float2bfloat16(v[j]);
+            }
+          }
+        } else {
+#pragma unroll
+          for (int j = 0; j < 16; ++j) part[(cc + j) * kBM + quad * 32 + lane] = v[j];
+        }
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&acc_empty[buf]);  // this warp's reads of the accumulator are done
+      if (whole || !live) continue;
+      // ---- stream-K fixup: the tile's last contributor sums all partials in CTA order ----
+      const int c_lo = sk.cta_of(t * sk.kb), c_hi = sk.cta_of((t + 1) * sk.kb - 1);
+      __threadfence();
+      asm volatile("bar.sync 1, 128;" ::: "memory");  // the 4 epilogue warps
+      if (et == 0) *last_flag = atomicAdd(&counters[c_lo], 1) == c_hi - c_lo;
+      asm volatile("bar.sync 1, 128;" ::: "memory");
+      if (*last_flag) {
+        __threadfence();
+        const int cg = et & 31, rp = et >> 5;  // 4 features (cg) x rows rp, rp + 4, ...
+        const int col = n0 + cg * 4;
+        const int m_end = min(M, m0 + BN);
+        if (col < N) {
+          for (int mb = m0 + rp; mb < m_end; mb += 16) {
+            float4 accv[4];
+#pragma unroll
+            for (int q = 0; q < 4; ++q) accv[q] = make_float4(0.f, 0.f, 0.f, 0.f);
+            for (int cc2 = c_lo; cc2 <= c_hi; ++cc2) {
+              const int first_tile = sk.start(cc2) / sk.kb;
+              const float* src = ws + (static_cast<size_t>(2 * cc2 + (t == first_tile ? 0 : 1)) * BN) * kBM;
+              float4 vv[4];
+#pragma unroll
+              for (int q = 0; q < 4; ++q) {
+                const int m = mb + 4 * q;
+                vv[q] = m < m_end ? __ldcg(reinterpret_cast<const float4*>(src + (m - m0) * kBM + cg * 4))
+                                  : make_float4(0.f, 0.f, 0.f, 0.f);
+              }
+#pragma unroll
+              for (int q = 0; q < 4; ++q) {
+                accv[q].x += vv[q].x; accv[q].y += vv[q].y; accv[q].z += vv[q].z; accv[q].w += vv[q].w;
+              }
+            }
+#pragma unroll
+            for (int q = 0; q < 4; ++q) {
+              const int m = mb + 4 * q;
+              if (m < m_end) {
+                __nv_bfloat162 lo = __floats2bfloat162_rn(accv[q].x, accv[q].y);
+                __nv_bfloat162 hi = __floats2bfloat162_rn(accv[q].z, accv[q].w);
+                uint2 packed;
+                packed.x = *reinterpret_cast<uint32_t*>(&lo);
+                packed.y = *reinterpret_cast<uint32_t*>(&hi);
+                *reinterpret_cast<uint2*>(y + static_cast<size_t>(m) * N + col) = packed;
+              }
+            }
+          }
+        }
+        if (et == 0) counters[c_lo] = 0;
+      }
+      asm volatile("bar.sync 1, 128;" ::: "memory");  // last_flag is reused by the next segment
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 0) tmem_dealloc(tmem, kTmemCols);
+}
+
+template <int BN>
+int run_gemm_persistent(const CUtensorMap& tm_w, const CUtensorMap& tm_x, void* y, float* ws, int* counters, int M,
+                        int N, int K, int ctas, unsigned* status, cudaStream_t stream) {
+  using Cfg = GemmCfg<BN>;
+  static bool configured = false;
+  if (!configured) {
+    cudaFuncSetAttribute(gemm_persistent_kernel<BN>, cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg::kSmem);
+    configured = true;
+  }
+  launch_pdl(gemm_persistent_kernel<BN>, dim3(ctas), dim3(192), Cfg::kSmem, stream, tm_w, tm_x,
+             static_cast<bf16*>(y), ws, counters, M, N, K, status);
+  return 0;
+}
+
 }  // namespace
 
 int gemm_block_n(int M) {
@@ -269,6 +505,28 @@ int gemm_splits(int M, int N, int K, int num_sms) {
   int splits = num_sms / tiles;
   splits = std::min(splits, total_kb / 4);
   return std::max(1, std::min(splits, 16));
+}
+
+int gemm_persistent_ctas(int M, int N, int K, int num_sms) {
+  const int bn = gemm_block_n(M);
+  const long units = static_cast<long>((N + kBM - 1) / kBM) * ((M + bn - 1) / bn) * ((K + kBK - 1) / kBK);
+  return static_cast<int>(std::min<long>(num_sms, units));
+}
+
+long gemm_persistent_ws_floats(int M, int N, int K, int num_sms) {
+  return 2L * gemm_persistent_ctas(M, N, K, num_sms) * gemm_block_n(M) * kBM;
+}
+
+int launch_gemm_persistent(const CUtensorMap* tm_w, const CUtensorMap* tm_x, void* y, float* ws, int* counters, int M,
+                           int N, int K, int num_sms, unsigned* status, cudaStream_t stream) {
+  if (K % 8 != 0 || N % 4 != 0 || counters == nullptr || ws == nullptr) return -1;
+  const int ctas = gemm_persistent_ctas(M, N, K, num_sms);
+  switch (gemm_block_n(M)) {
+    case 32: return run_gemm_persistent<32>(*tm_w, *tm_x, y, ws, counters, M, N, K, ctas, status, stream);
+    case 64: return run_gemm_persistent<64>(*tm_w, *tm_x, y, ws, counters, M, N, K, ctas, status, stream);
+    case 128: return run_gemm_persistent<128>(*tm_w, *tm_x, y, ws, counters, M, N, K, ctas, status, stream);
+    default: return run_gemm_persistent<256>(*tm_w, *tm_x, y, ws, counters, M, N, K, ctas, status, stream);
+  }
 }
 
 int launch_gemm_bf16(const CUtensorMap* tm_w, const CUtensorMap* tm_x, void* y, float* ws, int M, int N, int K,

@@ -38,6 +38,13 @@ int gemm_splits(int M, int N, int K, int num_sms);
 int launch_gemm_bf16(const CUtensorMap* tm_w, const CUtensorMap* tm_x, void* y, float* ws, int M, int N, int K,
                      int splits, unsigned* status, cudaStream_t stream, int* counters = nullptr);
 
+// Persistent stream-K GEMM: `ws` holds gemm_persistent_ws_floats() floats, `counters` >= num_sms zeroed ints
+// private to the stream (the kernel resets them).
+int gemm_persistent_ctas(int M, int N, int K, int num_sms);
+long gemm_persistent_ws_floats(int M, int N, int K, int num_sms);
+int launch_gemm_persistent(const CUtensorMap* tm_w, const CUtensorMap* tm_x, void* y, float* ws, int* counters, int M,
+                           int N, int K, int num_sms, unsigned* status, cudaStream_t stream);
+
 // attention.cu
 AttnPlan attention_plan(int B, int T, int H, int Hkv, int S, int num_sms);
 int launch_attention(const void* q, const CUtensorMap* tm_k, const CUtensorMap* tm_v, void* out, float* ws,

@@ -16,6 +16,7 @@ the following block, so capturing them costs nothing.
 
 from __future__ import annotations
 
+import math
 from typing import Any
 
 import torch
@@ -172,14 +173,18 @@ class CausalLM(nn.Module):
 
 
 @torch.no_grad()
-def init_weights(model: CausalLM, seed: int = 0, std: float = 0.02) -> CausalLM:
+def init_weights(model: CausalLM, seed: int = 0, std: float = 0.02, scaled_residual: bool = False) -> CausalLM:
     """Random initialisation N(0, std) of every matrix (norms at one), generated on the model's device from
-    ``seed`` in a fixed order, so two processes build identical weights."""
+    ``seed`` in a fixed order, so two processes build identical weights. With ``scaled_residual`` the output
+    projections of the residual branches (``wo``, ``w_down``) use ``std / sqrt(2 * num_layers)`` (the GPT-2 /
+    Megatron initialisation), which keeps a deep random model's residual stream from being dominated by noise."""
     gen = torch.Generator(device=model.device)
     gen.manual_seed(seed)
+    out_std = std / math.sqrt(2 * model.config.num_layers)
     for name, p in model.named_parameters():
         if p.dim() >= 2:
-            p.copy_(torch.randn(p.shape, generator=gen, device=p.device, dtype=torch.float32).mul_(std))
+            s = out_std if scaled_residual and name.rsplit(".", 1)[-1] in ("wo", "w_down") else std
+            p.copy_(torch.randn(p.shape, generator=gen, device=p.device, dtype=torch.float32).mul_(s))
         elif "norm" in name:
             p.fill_(1.0)
         else:

@@ -94,6 +94,34 @@ class Eagle3Technique(Technique):
         return ids
 
     @torch.no_grad()
+    def extend_draft_vocab(self, tokens: torch.Tensor, keep: torch.Tensor) -> int:
+        """Make every id of ``tokens`` draftable without disturbing the ids of ``keep`` (the ones the head was
+        trained on): missing ids replace draft slots whose id is not in ``keep``; their head rows start from the
+        target's. Returns the number of ids added."""
+        have = self.t2d.clone()
+        missing = torch.unique(tokens.reshape(-1).long().to(have.device))
+        missing = missing[~have[missing]]
+        if missing.numel() == 0:
+            return 0
+        ids = torch.arange(self.draft_vocab, device=have.device) + self.d2t
+        kept = torch.zeros_like(have)
+        kept[torch.unique(keep.reshape(-1).long().to(have.device))] = True
+        free = (~kept[ids]).nonzero().flatten()[: missing.numel()]
+        missing = missing[: free.numel()]
+        new_ids = ids.clone()
+        new_ids[free] = missing
+        order = torch.argsort(new_ids)
+        rows = self.lm_head.detach()[order].clone()
+        fresh = torch.isin(new_ids[order], missing)
+        rows[fresh] = self.model.head_weight.detach()[new_ids[order][fresh]].to(rows.dtype)
+        sorted_ids = new_ids[order]
+        self.d2t.copy_(sorted_ids - torch.arange(sorted_ids.numel(), device=sorted_ids.device))
+        self.t2d.zero_()
+        self.t2d[sorted_ids] = True
+        self.lm_head.copy_(rows)
+        return int(missing.numel())
+
+    @torch.no_grad()
     def set_draft_vocab(self, token_ids: torch.Tensor) -> None:
         """Restrict the own head to ``token_ids`` (``draft_vocab`` most frequent target tokens, any order)."""
         ids = token_ids.to(self.d2t.device).long().sort().values[: self.draft_vocab]
