@@ -22,7 +22,10 @@ from . import techniques  # noqa: F401  (registers the built-in techniques)
 from ._version import API_LEVEL, __version__
 from .core import CAPABILITY_ORDER, TECHNIQUES, Capability, Family, Simulation, Technique, TechniqueConfig, \
     register_technique, technique_for
+from .core.compatibility import compatibility_matrix, compatible, incompatibility, listed_techniques
 from .core.model import EfficientModel, apply, build_model
+from .core.serialization import (FORMATS, Checkpoint, CheckpointFormat, attach, from_pretrained, load,
+                                 read_checkpoint, save, teacher_fingerprint)
 from .decoding import DecodeConfig, DecodeResult, GreedySelector, SpecEngine, TokenSelector, TopPSampler
 from . import ops  # noqa: F401
 from .errors import (CalibrationMismatchWarning, CheckpointFormatError, CommTimeoutError, ConfigError,
@@ -32,7 +35,9 @@ from .errors import (CalibrationMismatchWarning, CheckpointFormatError, CommTime
                      UntestedEngineWarning)
 
 __all__ = [
-    "API_LEVEL", "CAPABILITY_ORDER", "TECHNIQUES", "CalibrationMismatchWarning", "Capability",
+    "API_LEVEL", "CAPABILITY_ORDER", "FORMATS", "TECHNIQUES", "Checkpoint", "CheckpointFormat", "attach",
+    "compatibility_matrix", "compatible", "from_pretrained", "incompatibility", "listed_techniques", "load",
+    "read_checkpoint", "save", "teacher_fingerprint", "CalibrationMismatchWarning", "Capability",
     "CheckpointFormatError", "CommTimeoutError", "ConfigError", "DecodeConfig", "DecodeResult", "DuplicateNameError",
     "EconomizeError", "EfficientModel", "Family", "GreedySelector", "IncompatibleTechniquesError",
     "KernelUnavailableError", "NonFiniteLossError", "SimulatedPathWarning", "Simulation", "SpecEngine", "Technique",

@@ -63,7 +63,7 @@ class EfficientModel(nn.Module):
         self.model = model
         self.techniques = nn.ModuleDict({t.name: t for t in techniques})
         self._base = [base_model if base_model is not None else model]
-        self._decoders: dict[DecodeConfig, SpecEngine] = {}
+        self._decoders: dict[tuple[DecodeConfig, str | None], SpecEngine] = {}
         self.decoding = decoding
         self.source_digests: dict[str, str] | None = None
 
@@ -136,10 +136,12 @@ class EfficientModel(nn.Module):
             raise ConfigError(f"decoding must be a DecodeConfig, got {type(config).__name__}")
         self._decoding = config
 
-    def decoder(self, decoding: DecodeConfig | None = None) -> SpecEngine:
-        """The engine for ``decoding`` (cached per configuration with its CUDA graphs)."""
+    def decoder(self, decoding: DecodeConfig | None = None, selector: Any = None) -> SpecEngine:
+        """The engine for ``decoding`` (cached per configuration and selector with its CUDA graphs)."""
         config = decoding or self.decoding
-        engine = self._decoders.get(config)
+        sampling = selector is not None and not getattr(selector, "greedy", True)
+        key = (config, repr(selector) if sampling else None)
+        engine = self._decoders.get(key)
         if engine is None:
             if config.lossless is True:
                 lossy = self.lossy_techniques(LOSSLESS_COMPATIBLE)
@@ -148,8 +150,8 @@ class EfficientModel(nn.Module):
             technique = self.drafting_technique
             drafter = technique.drafter() if technique is not None and config.cycle_length > 1 else None
             vocab = getattr(technique, "draft_vocab", None)
-            engine = SpecEngine(self.model, drafter, config, draft_vocab=vocab)
-            self._decoders[config] = engine
+            engine = SpecEngine(self.model, drafter, config, draft_vocab=vocab, selector=selector if sampling else None)
+            self._decoders[key] = engine
         return engine
 
     @torch.no_grad()
@@ -166,12 +168,8 @@ class EfficientModel(nn.Module):
                      decoding: DecodeConfig | None = None, stop: int | Sequence[int] | None = None,
                      selector: Any = None) -> list[DecodeResult]:
         config = decoding or self.decoding
-        if selector is not None and not getattr(selector, "greedy", True):
-            from ..decoding.sampling import sample_decode
-
-            return sample_decode(self, prompts, max_new_tokens, config, selector, stop)
         stops = [stop] if isinstance(stop, int) else (list(stop) if stop is not None else None)
-        return self.decoder(config).generate(prompts, max_new_tokens, stops)
+        return self.decoder(config, selector).generate(prompts, max_new_tokens, stops)
 
     def generate(self, inputs: torch.Tensor | None = None, *, max_new_tokens: int = 20,
                  decoding: DecodeConfig | None = None, input_ids: torch.Tensor | None = None,

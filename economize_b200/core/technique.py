@@ -135,6 +135,10 @@ class Technique(nn.Module):
     def technique_state(self) -> dict[str, torch.Tensor]:
         return {k: v.detach() for k, v in self.state_dict().items()}
 
+    def export_state(self) -> dict[str, torch.Tensor]:
+        """Tensors under economize's names (what checkpoints store); subclasses with fused layouts convert."""
+        return self.technique_state()
+
     def load_technique_state(self, state: dict[str, torch.Tensor]) -> None:
         missing, unexpected = self.load_state_dict(state, strict=False)
         if unexpected:

@@ -258,7 +258,8 @@ Tensor argmax(Tensor x) {
   return out;
 }
 
-std::tuple<Tensor, Tensor, Tensor> greedy_accept(Tensor tokens, Tensor parents, Tensor pred) {
+std::tuple<Tensor, Tensor, Tensor> greedy_accept(Tensor tokens, Tensor parents, Tensor pred,
+                                                 c10::optional<Tensor> ok) {
   CHECK_CUDA(tokens);
   CHECK_I64(tokens);
   CHECK_I64(parents);
@@ -271,9 +272,15 @@ std::tuple<Tensor, Tensor, Tensor> greedy_accept(Tensor tokens, Tensor parents, 
   auto n_acc = at::empty({B}, tokens.options().dtype(at::kInt));
   auto path = at::empty({B, T}, tokens.options().dtype(at::kInt));
   auto out = at::empty({B, T}, tokens.options());
+  Tensor okc;
+  if (ok.has_value()) {
+    okc = ok->to(at::kByte).contiguous();
+    TORCH_CHECK(okc.numel() == static_cast<int64_t>(B) * T, "ok must be [B, T]");
+  }
   const int rc = ecz::launch_greedy_accept(tokens.data_ptr<int64_t>(), parents.data_ptr<int64_t>(),
-                                           pred.data_ptr<int64_t>(), n_acc.data_ptr<int>(), path.data_ptr<int>(),
-                                           out.data_ptr<int64_t>(), B, T, at::cuda::getCurrentCUDAStream());
+                                           pred.data_ptr<int64_t>(), ok.has_value() ? okc.data_ptr<uint8_t>() : nullptr,
+                                           n_acc.data_ptr<int>(), path.data_ptr<int>(), out.data_ptr<int64_t>(), B, T,
+                                           at::cuda::getCurrentCUDAStream());
   TORCH_CHECK(rc == 0, "greedy_accept: at most 64 tree nodes");
   return {n_acc, path, out};
 }
@@ -296,6 +303,40 @@ void kv_compact(Tensor cache, Tensor kv_len, Tensor path, Tensor n_acc) {
                                         n_acc.data_ptr<int>(), LH, B, Hkv, S, D, T, std::min(max_depth, 64),
                                         at::cuda::getCurrentCUDAStream());
   TORCH_CHECK(rc == 0, "kv_compact: unsupported head_dim or path length");
+}
+
+Tensor sample(Tensor probs, Tensor u) {
+  CHECK_CUDA(probs);
+  TORCH_CHECK(probs.scalar_type() == at::kFloat && u.scalar_type() == at::kFloat, "sample takes fp32 probs and u");
+  c10::cuda::CUDAGuard guard(probs.device());
+  probs = probs.contiguous();
+  const int V = static_cast<int>(probs.size(-1));
+  const int rows = static_cast<int>(probs.numel() / V);
+  TORCH_CHECK(u.numel() == rows, "one uniform per row");
+  auto out = at::empty({rows}, probs.options().dtype(at::kLong));
+  ecz::launch_sample(probs.data_ptr<float>(), u.contiguous().data_ptr<float>(), out.data_ptr<int64_t>(), rows, V,
+                     at::cuda::getCurrentCUDAStream());
+  return out;
+}
+
+std::tuple<Tensor, Tensor> rejection(Tensor p, Tensor q, Tensor drafts, Tensor u_acc, Tensor u_draw) {
+  CHECK_CUDA(p);
+  TORCH_CHECK(p.scalar_type() == at::kFloat && q.scalar_type() == at::kFloat, "p and q must be fp32");
+  CHECK_I64(drafts);
+  c10::cuda::CUDAGuard guard(p.device());
+  p = p.contiguous();
+  q = q.contiguous();
+  drafts = drafts.contiguous();
+  const int B = static_cast<int>(drafts.size(0)), k = static_cast<int>(drafts.size(1));
+  const int V = static_cast<int>(p.size(-1));
+  TORCH_CHECK(p.numel() == static_cast<int64_t>(B) * (k + 1) * V && q.numel() == static_cast<int64_t>(B) * k * V,
+              "p [B, k+1, V], q [B, k, V]");
+  auto n_acc = at::empty({B}, drafts.options().dtype(at::kInt));
+  auto out = at::empty({B, k + 1}, drafts.options());
+  ecz::launch_rejection(p.data_ptr<float>(), q.data_ptr<float>(), drafts.data_ptr<int64_t>(),
+                        u_acc.contiguous().data_ptr<float>(), u_draw.contiguous().data_ptr<float>(),
+                        n_acc.data_ptr<int>(), out.data_ptr<int64_t>(), B, k, V, at::cuda::getCurrentCUDAStream());
+  return {n_acc, out};
 }
 
 int64_t status(int64_t device) {
@@ -328,8 +369,11 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("silu_mul", &silu_mul, "SwiGLU activation of [gate; up]");
   m.def("linear", &linear, "x @ w.T on tcgen05 (swap-AB, split-K)");
   m.def("argmax", &argmax, "row argmax");
-  m.def("greedy_accept", &greedy_accept, "longest accepted path of a verified draft tree");
+  m.def("greedy_accept", &greedy_accept, "longest accepted path of a verified draft tree", py::arg("tokens"),
+        py::arg("parents"), py::arg("pred"), py::arg("ok") = py::none());
   m.def("kv_compact", &kv_compact, "move an accepted path's K/V to consecutive slots");
+  m.def("sample", &sample, "inverse-CDF draw of one token per probability row");
+  m.def("rejection", &rejection, "lossless speculative sampling of a draft chain (accept/reject + resample)");
   m.def("status", &status, "read and clear the device status word of bounded waits");
   m.def("attention_plan", &attention_plan, "(m_tiles, splits, chunks_per_split) of an attention launch");
   m.def("gemm_splits", &gemm_splits, "split-K factor of a GEMM launch");

@@ -330,8 +330,9 @@ int launch_argmax(const void* x, bool is_bf16, int64_t* out, float* part_v, int*
 // The deepest accepted node (first on ties) ends the path. Outputs n_acc [B], path [B, T] (node of the i-th path
 // position, padded with the last node) and out [B, T] (path tokens after the root, then the bonus pred[last]).
 __global__ void greedy_accept_kernel(const int64_t* __restrict__ tokens, const int64_t* __restrict__ parents,
-                                     const int64_t* __restrict__ pred, int* __restrict__ n_acc,
-                                     int* __restrict__ path, int64_t* __restrict__ out, int T) {
+                                     const int64_t* __restrict__ pred, const uint8_t* __restrict__ ok,
+                                     int* __restrict__ n_acc, int* __restrict__ path, int64_t* __restrict__ out,
+                                     int T) {
   pdl_trigger();
   pdl_wait();
   const int b = blockIdx.x;
@@ -348,10 +349,11 @@ __global__ void greedy_accept_kernel(const int64_t* __restrict__ tokens, const i
     int best = 0, best_depth = 0;
     for (int t = 1; t < T; ++t) {
       const int p = par[t];
-      const bool ok = p >= 0 && p < t && acc[p] && tk[t] == pr[p];
-      acc[t] = ok;
+      const bool match = ok != nullptr ? ok[static_cast<size_t>(b) * T + t] != 0 : tk[t] == pr[p];
+      const bool good = p >= 0 && p < t && acc[p] && match;
+      acc[t] = good;
       depth[t] = (p >= 0 && p < t) ? depth[p] + 1 : 0;
-      if (ok && depth[t] > best_depth) { best_depth = depth[t]; best = t; }
+      if (good && depth[t] > best_depth) { best_depth = depth[t]; best = t; }
     }
     n_acc[b] = best_depth;
     int node = best;
@@ -366,10 +368,10 @@ __global__ void greedy_accept_kernel(const int64_t* __restrict__ tokens, const i
   }
 }
 
-int launch_greedy_accept(const int64_t* tokens, const int64_t* parents, const int64_t* pred, int* n_acc, int* path,
-                         int64_t* out, int B, int T, cudaStream_t stream) {
+int launch_greedy_accept(const int64_t* tokens, const int64_t* parents, const int64_t* pred, const uint8_t* ok,
+                         int* n_acc, int* path, int64_t* out, int B, int T, cudaStream_t stream) {
   if (T > 64) return -1;
-  launch_pdl(greedy_accept_kernel, dim3(B), dim3(32), 0, stream, tokens, parents, pred, n_acc, path, out, T);
+  launch_pdl(greedy_accept_kernel, dim3(B), dim3(32), 0, stream, tokens, parents, pred, ok, n_acc, path, out, T);
   return 0;
 }
 

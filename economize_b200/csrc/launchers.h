@@ -25,8 +25,9 @@ int launch_silu_mul(const void* gu, void* out, int rows, int F, cudaStream_t str
 int argmax_slices(int rows, int V);
 int launch_argmax(const void* x, bool is_bf16, int64_t* out, float* part_v, int* part_i, int rows, int V,
                   cudaStream_t stream);
-int launch_greedy_accept(const int64_t* tokens, const int64_t* parents, const int64_t* pred, int* n_acc, int* path,
-                         int64_t* out, int B, int T, cudaStream_t stream);
+// ok [B, T] (optional): node t is acceptable given its parent; without it, tokens[t] == pred[parent].
+int launch_greedy_accept(const int64_t* tokens, const int64_t* parents, const int64_t* pred, const uint8_t* ok,
+                         int* n_acc, int* path, int64_t* out, int B, int T, cudaStream_t stream);
 int launch_kv_compact(void* cache, const int* kv_len, const int* path, const int* n_acc, int LH, int B, int Hkv,
                       int S, int D, int T, int max_depth, cudaStream_t stream);
 
@@ -51,6 +52,11 @@ int launch_attention(const void* q, const CUtensorMap* tm_k, const CUtensorMap* 
                      const int* kv_len, const int* n_new, const int64_t* mask, int B, int T, int H, int Hkv, int D,
                      int S, float scale, int q_offset, const AttnPlan& plan, unsigned* status, cudaStream_t stream,
                      unsigned long long* trace = nullptr);
+
+// sampling.cu
+int launch_sample(const float* probs, const float* u, int64_t* out, int rows, int V, cudaStream_t stream);
+int launch_rejection(const float* p, const float* q, const int64_t* drafts, const float* u_acc, const float* u_draw,
+                     int* n_acc, int64_t* out, int B, int k, int V, cudaStream_t stream);
 
 // tmap.cpp: a 2-D bf16 tensor map over a row-major [rows, cols] matrix with a {64, box_rows} box and the 128-byte
 // swizzle (cols * 2 bytes must be a multiple of 16). Returns 0 on success.

@@ -29,7 +29,9 @@ from ..models.llama import CausalLM
 from ..runtime.cache import KVCache, StepBatch
 from .config import DecodeConfig
 from .drafter import DraftModel
+from .policies import POLICIES, ConfidencePolicy, DynamicTreePolicy
 from .tree import LOGP_FLOOR, TreeOptions, ancestor_bits, popcount64, select_candidates
+from .verifiers import VERIFIERS, RejectionVerifier, TypicalVerifier
 
 __all__ = ["DecodeResult", "GenerationStats", "SpecEngine"]
 
@@ -111,21 +113,23 @@ class SpecEngine:
     """
 
     def __init__(self, model: CausalLM, drafter: DraftModel | None, config: DecodeConfig,
-                 draft_vocab: int | None = None) -> None:
+                 draft_vocab: int | None = None, selector=None) -> None:
         self.model = model
         self.config = config
         self.drafter = drafter if config.cycle_length > 1 else None
         self.draft_vocab = draft_vocab or model.config.vocab_size
-        if config.verifier_name not in ("greedy", "accept_all"):
-            raise ConfigError(f"the engine verifies greedily; verifier {config.verifier_name!r} runs through the "
-                              "sampling decoder (economize_b200.decoding.sampling)")
+        self.selector = selector if selector is not None and not getattr(selector, "greedy", True) else None
+        self.verifier = VERIFIERS.get(config.verifier_name)(config)
+        self.policy = POLICIES.get(config.draft_policy_name)(config)
         self.accept_all = config.verifier_name == "accept_all"
-        policy = config.draft_policy_name
         self.tree: TreeOptions | None = None
-        if self.drafter is not None and policy == "dynamic_tree":
-            self.tree = TreeOptions.from_options(config.draft_policy_options, config.cycle_length)
-        elif policy not in ("fixed", "confidence", "dynamic_tree"):
-            raise ConfigError(f"unknown draft policy {policy!r}")
+        if self.drafter is not None and isinstance(self.policy, DynamicTreePolicy):
+            if not self.verifier.supports_trees or self.verifier.needs_draft_probs:
+                raise ConfigError(f"draft_policy 'dynamic_tree' drafts trees, which verifier "
+                                  f"{config.verifier_name!r} cannot verify; use greedy or typical")
+            self.tree = self.policy.options
+        self.rejection = isinstance(self.verifier, RejectionVerifier) and self.selector is not None
+        self.min_confidence = self.policy.min_confidence if isinstance(self.policy, ConfidencePolicy) else None
         if self.drafter is None:
             self.depth = 0
             self.nodes = 0
@@ -216,7 +220,7 @@ class SpecEngine:
         last_idx = (lengths.long() - 1).clamp_min(0)
         rows = torch.arange(batch, device=prompts.device)
         logits = model.logits(hidden[rows, last_idx])
-        bonus = ops.argmax(logits)
+        bonus = self._choose(logits)
         st.kv_len.copy_(lengths)
         st.last.copy_(bonus)
         st.out.zero_()
@@ -303,7 +307,7 @@ class SpecEngine:
         sb = StepBatch(st.kv_len, one, st.kv_len[:, None].contiguous(),
                        torch.ones(batch, 1, dtype=torch.int64, device=st.kv_len.device))
         hidden, _ = model.forward_step(st.last[:, None], sb, st.cache)
-        pred = ops.argmax(model.logits(hidden[:, 0]))
+        pred = self._choose(model.logits(hidden[:, 0]))
         active = st.n_out < st.max_new
         st.out.scatter_(1, torch.where(active, st.n_out, st.out_cap).long()[:, None], pred[:, None])
         st.n_out.add_(1)
@@ -315,10 +319,11 @@ class SpecEngine:
         model, drafter = self.model, self.drafter
         batch, dev = st.batch, st.kv_len.device
         depth = self.depth
+        q_full = None
         if self.tree is not None:
             draft_tokens, draft_parents = self._draft_tree(st)
         else:
-            draft_tokens, draft_parents = self._draft_chain(st)
+            draft_tokens, draft_parents, q_full = self._draft_chain(st)
         # ---- verify: root + drafts in one tree pass ----
         tokens = torch.cat([st.last[:, None], draft_tokens], 1)  # [B, T]
         length = tokens.shape[1]
@@ -327,14 +332,9 @@ class SpecEngine:
         positions = (st.kv_len[:, None] + (popcount64(bits) - 1)).to(torch.int32)
         n_new = torch.full((batch,), length, dtype=torch.int32, device=dev)
         sb = StepBatch(st.kv_len, n_new, positions, bits)
-        hidden, aux = model.forward_step(tokens, sb, st.cache, drafter.capture_layers)
-        if self.accept_all:
-            pred = ops.argmax(model.logits(hidden))
-            pred = torch.where(torch.arange(length, device=dev)[None] < length - 1,
-                               torch.cat([draft_tokens, pred[:, -1:]], 1), pred)
-        else:
-            pred = ops.argmax(model.logits(hidden))  # [B, T]
-        n_acc, path, out = ops.greedy_accept(tokens, parents, pred)
+        hidden, aux = model.forward_step(tokens.clamp_min(0), sb, st.cache, drafter.capture_layers)
+        logits = model.logits(hidden)  # [B, T, V]
+        n_acc, path, out = self._verify(tokens, parents, logits, draft_tokens, q_full)
         ops.kv_compact(st.cache.data, st.kv_len, path, n_acc)
         # ---- commit ----
         active = st.n_out < st.max_new
@@ -362,23 +362,85 @@ class SpecEngine:
         st.root_state.copy_(root_state)
 
     # ---- drafting ----------------------------------------------------------------------------------------------
-    def _draft_chain(self, st: _State) -> tuple[torch.Tensor, torch.Tensor]:
+    def _draft_step_choice(self, logits: torch.Tensor) -> tuple[torch.Tensor, torch.Tensor | None, torch.Tensor]:
+        """A chain draft from draft-vocabulary logits ``[B, V_d]``: the target id, the draft distribution over the
+        target vocabulary (rejection sampling only) and the drafter's top probability."""
+        drafter = self.drafter
+        if self.rejection:
+            q = self.selector.probs(logits)
+            u = torch.rand(q.shape[0], device=q.device)
+            d = ops.sample(q.contiguous(), u)
+            tok = drafter.to_target(d)
+            ids = drafter.to_target(torch.arange(q.shape[-1], device=q.device))
+            q_full = torch.zeros(q.shape[0], self.model.config.vocab_size, device=q.device)
+            q_full[:, ids] = q
+            return tok, q_full, q.gather(1, d[:, None])[:, 0]
+        d = ops.argmax(logits)
+        top = torch.softmax(logits.float(), -1).gather(1, d[:, None])[:, 0] if self.min_confidence else logits[:, 0]
+        return drafter.to_target(d), None, top
+
+    def _draft_chain(self, st: _State) -> tuple[torch.Tensor, torch.Tensor, torch.Tensor | None]:
         drafter = self.drafter
         batch, dev = st.batch, st.kv_len.device
         k = self.depth
-        tok = drafter.to_target(ops.argmax(st.root_logits))
-        tokens = [tok]
+        tok, q, conf = self._draft_step_choice(st.root_logits)
+        tokens, qs, confs = [tok], [q], [conf]
         state = st.root_state[:, None]
         base = st.kv_len + 1
         for d in range(1, k):
             bits = torch.full((batch, 1), (1 << d) - 1, dtype=torch.int64, device=dev)
             pos = (st.kv_len + d).to(torch.int32)[:, None]
             logits, out = drafter.tree_step(tok[:, None], state, pos, base, d, d - 1, bits)
-            tok = drafter.to_target(ops.argmax(logits[:, 0]))
+            tok, q, conf = self._draft_step_choice(logits[:, 0])
             state = out
             tokens.append(tok)
+            qs.append(q)
+            confs.append(conf)
+        drafts = torch.stack(tokens, 1)
+        if self.min_confidence is not None:
+            # stop after the first draft whose confidence is below the threshold (the first draft always stays)
+            low = torch.stack(confs, 1) < self.min_confidence
+            stop = torch.cumsum(low.int(), 1) - low.int() > 0  # a low-confidence draft before this one
+            stop[:, 0] = False
+            drafts = torch.where(stop, torch.full_like(drafts, -1), drafts)
         parents = (torch.arange(k, device=dev) - 1).expand(batch, k).contiguous()  # -1: child of the root
-        return torch.stack(tokens, 1), parents
+        q_full = torch.stack(qs, 1) if self.rejection else None
+        return drafts, parents, q_full
+
+    # ---- verification ------------------------------------------------------------------------------------------
+    def _choose(self, logits: torch.Tensor) -> torch.Tensor:
+        """The exact model's token after every row of ``logits [..., V]``: argmax, or a draw from the selector."""
+        if self.selector is None:
+            return ops.argmax(logits)
+        probs = self.selector.probs(logits)
+        u = torch.rand(probs.shape[:-1], device=probs.device)
+        return ops.sample(probs.contiguous(), u)
+
+    def _verify(self, tokens: torch.Tensor, parents: torch.Tensor, logits: torch.Tensor, drafts: torch.Tensor,
+                q_full: torch.Tensor | None) -> tuple[torch.Tensor, torch.Tensor, torch.Tensor]:
+        batch, length = tokens.shape
+        dev = tokens.device
+        if self.rejection:
+            p = self.selector.probs(logits).contiguous()  # [B, k + 1, V]
+            k = drafts.shape[1]
+            n_acc, out = ops.rejection(p, q_full.contiguous(), drafts.clamp_min(0),
+                                       torch.rand(batch, k, device=dev), torch.rand(batch, device=dev))
+            if self.min_confidence is not None:  # invalidated drafts are never kept
+                limit = (drafts >= 0).int().cumprod(1).sum(1).to(torch.int32)
+                n_acc = torch.minimum(n_acc, limit)
+            path = torch.arange(length, device=dev, dtype=torch.int32).expand(batch, length)
+            path = torch.minimum(path, n_acc[:, None]).contiguous()
+            return n_acc, path, out
+        pred = self._choose(logits)  # [B, T]
+        if self.accept_all:
+            pred = torch.cat([drafts.clamp_min(0), pred[:, -1:]], 1)
+            return ops.greedy_accept(tokens, parents, pred)
+        if isinstance(self.verifier, TypicalVerifier):
+            probs = torch.softmax(logits.float(), -1)
+            parent_probs = probs.gather(1, parents[..., None].expand(batch, length, probs.shape[-1]))
+            ok = self.verifier.acceptable(parent_probs, tokens) & (tokens >= 0)
+            return ops.greedy_accept(tokens, parents, pred, ok)
+        return ops.greedy_accept(tokens, parents, pred)
 
     def _draft_tree(self, st: _State) -> tuple[torch.Tensor, torch.Tensor]:
         drafter, tree = self.drafter, self.tree

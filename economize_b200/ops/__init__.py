@@ -22,7 +22,9 @@ __all__ = [
     "load_error",
     "require",
     "rmsnorm",
+    "rejection",
     "rope_store",
+    "sample",
     "silu_mul",
 ]
 
@@ -82,12 +84,12 @@ def argmax(x: torch.Tensor) -> torch.Tensor:
     return x.argmax(-1)
 
 
-def greedy_accept(tokens: torch.Tensor, parents: torch.Tensor, pred: torch.Tensor
-                  ) -> tuple[torch.Tensor, torch.Tensor, torch.Tensor]:
-    """Longest accepted path of a greedily verified chain or tree (see :func:`.reference.greedy_accept`)."""
+def greedy_accept(tokens: torch.Tensor, parents: torch.Tensor, pred: torch.Tensor,
+                  ok: torch.Tensor | None = None) -> tuple[torch.Tensor, torch.Tensor, torch.Tensor]:
+    """Longest accepted path of a verified chain or tree (see :func:`.reference.greedy_accept`)."""
     if tokens.is_cuda:
-        return require().greedy_accept(tokens, parents, pred)
-    return reference.greedy_accept(tokens, parents, pred)
+        return require().greedy_accept(tokens, parents, pred, ok)
+    return reference.greedy_accept(tokens, parents, pred, ok)
 
 
 def kv_compact(cache: torch.Tensor, kv_len: torch.Tensor, path: torch.Tensor, n_acc: torch.Tensor) -> None:
@@ -96,3 +98,20 @@ def kv_compact(cache: torch.Tensor, kv_len: torch.Tensor, path: torch.Tensor, n_
         require().kv_compact(cache, kv_len, path, n_acc)
         return
     reference.kv_compact(cache, kv_len, path, n_acc)
+
+
+def sample(probs: torch.Tensor, u: torch.Tensor) -> torch.Tensor:
+    """One token per row of ``probs [..., V]`` (fp32) by inverse CDF at the uniforms ``u [...]``."""
+    if probs.is_cuda:
+        shape = probs.shape[:-1]
+        return require().sample(probs.reshape(-1, probs.shape[-1]).float(), u.reshape(-1).float()).reshape(shape)
+    return reference.sample(probs, u)
+
+
+def rejection(p: torch.Tensor, q: torch.Tensor, drafts: torch.Tensor, u_acc: torch.Tensor,
+              u_draw: torch.Tensor) -> tuple[torch.Tensor, torch.Tensor]:
+    """Lossless speculative sampling of draft chains: accept/reject every draft and draw the correction or bonus
+    token in one kernel (see :func:`.reference.rejection`)."""
+    if p.is_cuda:
+        return require().rejection(p.float(), q.float(), drafts, u_acc.float(), u_draw.float())
+    return reference.rejection(p, q, drafts, u_acc, u_draw)

@@ -13,6 +13,8 @@ import torch.nn.functional as F
 
 __all__ = [
     "attention",
+    "rejection",
+    "sample",
     "greedy_accept",
     "kv_compact",
     "linear",
@@ -123,7 +125,7 @@ def linear(x: torch.Tensor, weight: torch.Tensor, bias: torch.Tensor | None = No
     return F.linear(x, weight, bias)
 
 
-def greedy_accept(tokens: torch.Tensor, parents: torch.Tensor, pred: torch.Tensor
+def greedy_accept(tokens: torch.Tensor, parents: torch.Tensor, pred: torch.Tensor, ok: torch.Tensor | None = None
                   ) -> tuple[torch.Tensor, torch.Tensor, torch.Tensor]:
     """Longest accepted path of a verified draft tree.
 
@@ -132,6 +134,7 @@ def greedy_accept(tokens: torch.Tensor, parents: torch.Tensor, pred: torch.Tenso
             drafts in topological order.
         parents: ``[B, T]`` parent node of every node (``parents[:, 0]`` is ignored); a chain has ``parents[t] = t-1``.
         pred: ``[B, T]`` the exact model's choice after every node.
+        ok: optional ``[B, T]`` bools replacing the match rule: node ``t`` is acceptable given its parent.
 
     Returns:
         ``n_acc [B]`` accepted drafts, ``path [B, T]`` node index of the path's ``i``-th node (``path[:, 0] = 0``,
@@ -146,8 +149,8 @@ def greedy_accept(tokens: torch.Tensor, parents: torch.Tensor, pred: torch.Tenso
     for t in range(1, length):
         p = parents[:, t].long().clamp_min(0)
         par_acc = acc.gather(1, p[:, None])[:, 0]
-        ok = par_acc & (tokens[:, t] == pred.gather(1, p[:, None])[:, 0]) & (parents[:, t] >= 0)
-        acc[:, t] = ok
+        match = ok[:, t].bool() if ok is not None else tokens[:, t] == pred.gather(1, p[:, None])[:, 0]
+        acc[:, t] = par_acc & match & (parents[:, t] >= 0)
         depth[:, t] = depth.gather(1, p[:, None])[:, 0] + 1
     score = torch.where(acc, depth, torch.full_like(depth, -1))
     # deepest accepted node, first one on ties
@@ -182,3 +185,48 @@ def kv_compact(cache: torch.Tensor, kv_len: torch.Tensor, path: torch.Tensor, n_
         src = base + path[b, : n + 1].long()
         moved = cache[:, :, b, :, src].clone()
         cache[:, :, b, :, base:base + n + 1] = moved
+
+
+def _draw(weights: torch.Tensor, u: float) -> int:
+    total = float(weights.sum())
+    if total <= 0:
+        return -1
+    cdf = torch.cumsum(weights.double(), 0)
+    idx = int(torch.searchsorted(cdf, torch.tensor([u * float(cdf[-1])], dtype=torch.float64), right=True))
+    idx = min(idx, weights.numel() - 1)
+    while idx > 0 and weights[idx] <= 0:
+        idx -= 1
+    return idx
+
+
+def sample(probs: torch.Tensor, u: torch.Tensor) -> torch.Tensor:
+    """One token per row of ``probs [..., V]`` by inverse CDF at ``u [...]``."""
+    flat = probs.reshape(-1, probs.shape[-1])
+    out = [max(_draw(flat[i], float(u.reshape(-1)[i])), 0) for i in range(flat.shape[0])]
+    return torch.tensor(out, dtype=torch.int64, device=probs.device).reshape(probs.shape[:-1])
+
+
+def rejection(p: torch.Tensor, q: torch.Tensor, drafts: torch.Tensor, u_acc: torch.Tensor,
+              u_draw: torch.Tensor) -> tuple[torch.Tensor, torch.Tensor]:
+    """Lossless speculative sampling of draft chains (see ``csrc/sampling.cu``): ``n_acc [B]`` and ``out [B, k+1]``
+    (accepted drafts, then the correction or bonus token)."""
+    batch, k = drafts.shape
+    n_acc = torch.zeros(batch, dtype=torch.int32, device=p.device)
+    out = torch.zeros(batch, k + 1, dtype=torch.int64, device=p.device)
+    for b in range(batch):
+        j = 0
+        while j < k:
+            x = int(drafts[b, j])
+            if not float(u_acc[b, j]) * float(q[b, j, x]) < float(p[b, j, x]):
+                break
+            out[b, j] = x
+            j += 1
+        if j < k:
+            tok = _draw((p[b, j] - q[b, j]).clamp_min(0), float(u_draw[b]))
+            if tok < 0:
+                tok = _draw(p[b, j], float(u_draw[b]))
+        else:
+            tok = _draw(p[b, k], float(u_draw[b]))
+        out[b, j] = max(tok, 0)
+        n_acc[b] = j
+    return n_acc, out

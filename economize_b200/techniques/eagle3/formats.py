@@ -88,3 +88,99 @@ def to_official_state(tech) -> dict[str, torch.Tensor]:
 
 def from_official_state(tech, state: dict[str, torch.Tensor]) -> None:
     from_reference_state(tech, state)
+
+
+# ---- the official checkpoint layout as a registered format ------------------------------------------------------
+def _flat(config: dict) -> dict:
+    layer = config.get("transformer_layer_config")
+    if not isinstance(layer, dict):
+        return config
+    return {**layer, **{k: v for k, v in config.items() if k != "transformer_layer_config" and v is not None}}
+
+
+def config_from_official(config: dict):
+    """The :class:`Eagle3Config` of an official / SpecForge / vLLM-speculators EAGLE-3 ``config.json``."""
+    from ...errors import CheckpointFormatError
+    from .config import Eagle3Config
+
+    config = _flat(config)
+    eagle = dict(config.get("eagle_config") or {})
+    for flag in ("norm_before_fc", "fc_norm", "norm_output", "input_norm"):
+        if config.get(flag) or eagle.get(flag):
+            raise CheckpointFormatError(f"the EAGLE-3 option {flag!r} is not supported")
+    hidden = int(config["hidden_size"])
+    target = config.get("target_hidden_size")
+    if target is not None and int(target) != hidden:
+        raise CheckpointFormatError(f"a draft width {hidden} other than the model's ({target}) is not supported")
+    heads = int(config["num_attention_heads"])
+    vocab, draft_vocab = config.get("vocab_size"), config.get("draft_vocab_size")
+    aux = eagle.get("eagle_aux_hidden_state_layer_ids") or config.get("eagle_aux_hidden_state_layer_ids")
+    return Eagle3Config(
+        aux_layers=tuple(int(i) for i in aux) if aux else None,
+        head="own",
+        draft_vocab=int(draft_vocab) if draft_vocab is not None and vocab is not None and draft_vocab < vocab else None,
+        intermediate_size=int(config["intermediate_size"]),
+        num_heads=heads,
+        num_kv_heads=int(config.get("num_key_value_heads") or heads),
+        head_dim=int(config.get("head_dim") or hidden // heads),
+        attention_bias=bool(config.get("attention_bias", False)),
+        rope_theta=float(config.get("rope_theta", 10000.0)),
+        rope_scaling=config.get("rope_scaling"),
+        rms_norm_eps=float(config.get("rms_norm_eps", 1e-6)),
+        norm_before_residual=bool(config.get("norm_before_residual", eagle.get("norm_before_residual", False))),
+    )
+
+
+class Eagle3Format:
+    """Official EAGLE-3 heads (SafeAILab, SpecForge, vLLM speculators): ``config.json`` + ``model.safetensors``
+    (or ``pytorch_model.bin``) with ``midlayer.*`` / ``layers.0.*``, ``fc``, ``norm``, ``lm_head``, ``d2t``, ``t2d``."""
+
+    files = ("model.safetensors", "pytorch_model.bin")
+
+    def detect(self, path) -> bool:
+        import json
+        from pathlib import Path
+
+        path = Path(path)
+        cfg = path / "config.json"
+        if not cfg.is_file() or not any((path / f).is_file() for f in self.files):
+            return False
+        data = json.loads(cfg.read_text())
+        arch = " ".join(data.get("architectures") or [])
+        return "draft_vocab_size" in _flat(data) or "Eagle3" in arch or "eagle3" in str(data.get("speculators_model_type", ""))
+
+    def read(self, path):
+        import json
+        from pathlib import Path
+
+        from ...core.serialization import Checkpoint
+
+        path = Path(path)
+        config = json.loads((path / "config.json").read_text())
+        if (path / "model.safetensors").is_file():
+            from safetensors.torch import load_file
+
+            state = load_file(str(path / "model.safetensors"))
+        else:
+            state = torch.load(path / "pytorch_model.bin", map_location="cpu", weights_only=True)
+        state = {k: v for k, v in state.items() if not k.startswith("embed_tokens")}
+        renamed = {}
+        for key, value in state.items():
+            for prefix in ("midlayer.", "layers.0."):
+                if key.startswith(prefix):
+                    key = "layer." + key[len(prefix):]
+            renamed[key] = value
+        cfg = config_from_official(config)
+        base = config.get("base_model_name_or_path") or ((config.get("speculators_config") or {}).get("verifier")
+                                                         or {}).get("name_or_path")
+        return Checkpoint([cfg], {"eagle3": renamed}, None, base, {"base_model": base})
+
+
+def _register() -> None:
+    from ...core.serialization import FORMATS
+
+    if "eagle3" not in FORMATS:
+        FORMATS.register("eagle3", Eagle3Format())
+
+
+_register()

@@ -138,6 +138,16 @@ class Eagle3Technique(Technique):
     def default_decoding(self) -> DecodeConfig:
         return DecodeConfig(cycle_length=4)
 
+    def export_state(self) -> dict[str, torch.Tensor]:
+        from .formats import to_reference_state
+
+        return to_reference_state(self)
+
+    def load_technique_state(self, state: dict[str, torch.Tensor]) -> None:
+        from .formats import from_reference_state
+
+        from_reference_state(self, state)
+
     def drafter(self) -> Eagle3Drafter:
         return Eagle3Drafter(self)
 

@@ -181,3 +181,33 @@ def test_greedy_accept_and_compact(cuda):
     got = cache.to(cuda)
     ops.kv_compact(got, kv_len.to(cuda), path, n)
     assert torch.equal(got.cpu(), exp)
+
+
+def test_sample_kernel_matches_reference(cuda):
+    g = torch.Generator(device=cuda).manual_seed(10)
+    probs = torch.softmax(torch.randn(33, 128256, device=cuda, generator=g) * 3, -1)
+    u = torch.rand(33, device=cuda, generator=g)
+    got = ops.sample(probs, u)
+    want = ref.sample(probs.double().cpu(), u.cpu())
+    # inverse CDF in fp32 vs fp64: equal, or adjacent in the support at a CDF boundary
+    diff = (got.cpu() != want).sum().item()
+    assert diff <= 1
+
+
+def test_rejection_kernel_matches_reference(cuda):
+    g = torch.Generator().manual_seed(11)
+    B, k, V = 16, 4, 4096
+    p = torch.softmax(torch.randn(B, k + 1, V, generator=g), -1)
+    q = torch.softmax(torch.randn(B, k, V, generator=g) * 2, -1)
+    drafts = torch.multinomial(q.reshape(-1, V), 1, generator=g).reshape(B, k)
+    # make some drafts near-certain accepts
+    p[:, :k].scatter_(2, drafts[..., None], 0.5)
+    p = p / p.sum(-1, keepdim=True)
+    u_acc, u_draw = torch.rand(B, k, generator=g), torch.rand(B, generator=g)
+    n_ref, out_ref = ref.rejection(p.double(), q.double(), drafts, u_acc.double(), u_draw.double())
+    n_got, out_got = ops.rejection(p.to(cuda), q.to(cuda), drafts.to(cuda), u_acc.to(cuda), u_draw.to(cuda))
+    assert torch.equal(n_got.cpu(), n_ref)
+    for b in range(B):
+        j = int(n_ref[b])
+        assert torch.equal(out_got[b, :j].cpu(), out_ref[b, :j])
+        assert abs(int(out_got[b, j]) - int(out_ref[b, j])) <= 1 or out_got[b, j] == out_ref[b, j]
