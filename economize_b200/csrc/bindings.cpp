@@ -339,6 +339,20 @@ std::tuple<Tensor, Tensor> rejection(Tensor p, Tensor q, Tensor drafts, Tensor u
   return {n_acc, out};
 }
 
+Tensor ngram(Tensor history, Tensor len, int64_t k, int64_t min_n, int64_t max_n, bool earliest) {
+  CHECK_CUDA(history);
+  CHECK_I64(history);
+  CHECK_I32(len);
+  c10::cuda::CUDAGuard guard(history.device());
+  history = history.contiguous();
+  const int B = static_cast<int>(history.size(0)), cap = static_cast<int>(history.size(1));
+  auto drafts = at::empty({B, k}, history.options());
+  ecz::launch_ngram(history.data_ptr<int64_t>(), len.contiguous().data_ptr<int>(), drafts.data_ptr<int64_t>(), B, cap,
+                    static_cast<int>(k), static_cast<int>(min_n), static_cast<int>(max_n), earliest,
+                    at::cuda::getCurrentCUDAStream());
+  return drafts;
+}
+
 int64_t status(int64_t device) {
   const at::Device dev(at::kCUDA, static_cast<c10::DeviceIndex>(device));
   c10::cuda::CUDAGuard guard(dev);
@@ -374,6 +388,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("kv_compact", &kv_compact, "move an accepted path's K/V to consecutive slots");
   m.def("sample", &sample, "inverse-CDF draw of one token per probability row");
   m.def("rejection", &rejection, "lossless speculative sampling of a draft chain (accept/reject + resample)");
+  m.def("ngram", &ngram, "prompt-lookup draft proposals from the token history");
   m.def("status", &status, "read and clear the device status word of bounded waits");
   m.def("attention_plan", &attention_plan, "(m_tiles, splits, chunks_per_split) of an attention launch");
   m.def("gemm_splits", &gemm_splits, "split-K factor of a GEMM launch");

@@ -58,6 +58,10 @@ int launch_sample(const float* probs, const float* u, int64_t* out, int rows, in
 int launch_rejection(const float* p, const float* q, const int64_t* drafts, const float* u_acc, const float* u_draw,
                      int* n_acc, int64_t* out, int B, int k, int V, cudaStream_t stream);
 
+// ngram.cu
+int launch_ngram(const int64_t* history, const int* len, int64_t* drafts, int B, int cap, int k, int min_n, int max_n,
+                 bool earliest, cudaStream_t stream);
+
 // tmap.cpp: a 2-D bf16 tensor map over a row-major [rows, cols] matrix with a {64, box_rows} box and the 128-byte
 // swizzle (cols * 2 bytes must be a multiple of 16). Returns 0 on success.
 int make_tmap_2d_bf16(CUtensorMap* map, const void* base, uint64_t rows, uint64_t cols, uint64_t row_stride_elems,

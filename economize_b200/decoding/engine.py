@@ -95,6 +95,8 @@ class _State:
         self.max_new = torch.zeros(batch, **i32)
         self.accepted = torch.zeros(batch, dtype=torch.int64, device=dev)
         self.cycles = torch.zeros(batch, **i32)
+        # prompt + committed tokens + the pending root, slot p = position p (read by n-gram drafters)
+        self.history = torch.zeros(batch, capacity + 1, dtype=torch.int64, device=dev)
         hidden = model.config.hidden_size
         if drafter is not None:
             self.carry = torch.zeros(batch, max(drafter.carry_size, 1), dtype=model.dtype, device=dev)
@@ -130,9 +132,14 @@ class SpecEngine:
             self.tree = self.policy.options
         self.rejection = isinstance(self.verifier, RejectionVerifier) and self.selector is not None
         self.min_confidence = self.policy.min_confidence if isinstance(self.policy, ConfidencePolicy) else None
+        self.static = self.drafter is not None and hasattr(self.drafter, "propose")
         if self.drafter is None:
             self.depth = 0
             self.nodes = 0
+        elif self.static:
+            self.tree = None
+            self.depth = self.drafter.draft_depth(config)
+            self.nodes = self.drafter.draft_nodes(config)
         elif self.tree is not None:
             self.depth = self.tree.depth
             self.nodes = self.tree.total_tokens
@@ -223,19 +230,23 @@ class SpecEngine:
         bonus = self._choose(logits)
         st.kv_len.copy_(lengths)
         st.last.copy_(bonus)
+        st.history.zero_()
+        st.history[:, :width] = prompts
+        st.history[rows, lengths.long()] = bonus
         st.out.zero_()
         st.out[:, 0] = bonus
         st.n_out.fill_(1)
         st.max_new.copy_(max_new)
-        if drafter is not None:
+        if drafter is not None and getattr(drafter, "observes", True):
             fused = drafter.fuse(aux)  # [B, P, d]
             tokens = torch.cat([prompts, torch.zeros_like(prompts[:, :1])], 1)
             tokens[rows, lengths.long()] = bonus
             sources = torch.cat([torch.zeros_like(fused[:, :1]), fused], 1)
             n_valid = lengths + 1
             root_logits, root_state = drafter.observe(tokens, sources, torch.zeros_like(lengths), n_valid, lengths)
-            st.root_logits.copy_(root_logits)
-            st.root_state.copy_(root_state)
+            if root_logits is not None:
+                st.root_logits.copy_(root_logits)
+                st.root_state.copy_(root_state)
             st.carry.copy_(fused[rows, last_idx])
 
     def _chunked_prefill(self, st: _State, prompts: torch.Tensor, lengths: torch.Tensor, chunk: int,
@@ -320,7 +331,9 @@ class SpecEngine:
         batch, dev = st.batch, st.kv_len.device
         depth = self.depth
         q_full = None
-        if self.tree is not None:
+        if self.static:
+            draft_tokens, draft_parents = drafter.propose(st.history, st.kv_len + 1)
+        elif self.tree is not None:
             draft_tokens, draft_parents = self._draft_tree(st)
         else:
             draft_tokens, draft_parents, q_full = self._draft_chain(st)
@@ -345,6 +358,15 @@ class SpecEngine:
         st.out.scatter_(1, torch.where(keep, idx, st.out_cap), out[:, :width])
         st.accepted.add_(torch.where(active, n_acc, 0).long())
         st.cycles.add_(active.int())
+        hist_idx = st.kv_len.long()[:, None] + 1 + col
+        hist_keep = (col <= n_acc.long()[:, None]) & (hist_idx < st.history.shape[1])
+        st.history.scatter_(1, torch.where(hist_keep, hist_idx, st.history.shape[1] - 1), out[:, :width])
+        rows = torch.arange(batch, device=dev)
+        if not getattr(drafter, "observes", True):
+            st.last.copy_(out[rows, n_acc.long()])
+            st.kv_len.add_(n_acc + 1)
+            st.n_out.add_(n_acc + 1)
+            return
         # ---- observe: drafter state for the committed columns + next root step ----
         path_w = path[:, :width].long()
         aux_path = {k: v.gather(1, path_w[..., None].expand(batch, width, v.shape[-1])) for k, v in aux.items()}
@@ -353,13 +375,13 @@ class SpecEngine:
         sources = torch.cat([st.carry[:, None].to(fused.dtype), fused], 1)
         n_valid = (n_acc + 2).to(torch.int32)
         root_logits, root_state = drafter.observe(obs_tokens, sources, st.kv_len, n_valid, n_valid - 1)
-        rows = torch.arange(batch, device=dev)
         st.carry.copy_(fused[rows, n_acc.long()])
         st.last.copy_(out[rows, n_acc.long()])
         st.kv_len.add_(n_acc + 1)
         st.n_out.add_(n_acc + 1)
-        st.root_logits.copy_(root_logits)
-        st.root_state.copy_(root_state)
+        if root_logits is not None:
+            st.root_logits.copy_(root_logits)
+            st.root_state.copy_(root_state)
 
     # ---- drafting ----------------------------------------------------------------------------------------------
     def _draft_step_choice(self, logits: torch.Tensor) -> tuple[torch.Tensor, torch.Tensor | None, torch.Tensor]:

@@ -112,7 +112,8 @@ class CausalLM(nn.Module):
                      capture: tuple[int, ...] = (), layers: range | None = None,
                      ) -> tuple[torch.Tensor, dict[int, torch.Tensor]]:
         """Run a pass over ``tokens [B, T]``; returns the final-normed hidden states ``[B, T, H]`` and the captured
-        block outputs ``{i: [B, T, H]}`` (``0``: the embeddings, ``i``: the output of ``i`` blocks)."""
+        block outputs ``{i: [B, T, H]}`` (``0``: the embeddings, ``i``: the output of ``i`` blocks, ``-1``: the
+        final-normed states again)."""
         c = self.config
         cos, sin = self.rope_tables()
         h = self.embed_tokens(tokens)
@@ -130,6 +131,8 @@ class CausalLM(nn.Module):
         out, resid = ops.rmsnorm(h, self.norm, c.rms_norm_eps, resid)
         if c.num_layers in capture:
             aux[c.num_layers] = resid
+        if -1 in capture:  # the final-normed hidden states (what the LM head reads)
+            aux[-1] = out
         return out, aux
 
     def _attention(self, layer: DecoderLayer, index: int, x: torch.Tensor, batch: StepBatch, cache: KVCache,

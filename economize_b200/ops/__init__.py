@@ -22,6 +22,7 @@ __all__ = [
     "load_error",
     "require",
     "rmsnorm",
+    "ngram",
     "rejection",
     "rope_store",
     "sample",
@@ -115,3 +116,11 @@ def rejection(p: torch.Tensor, q: torch.Tensor, drafts: torch.Tensor, u_acc: tor
     if p.is_cuda:
         return require().rejection(p.float(), q.float(), drafts, u_acc.float(), u_draw.float())
     return reference.rejection(p, q, drafts, u_acc, u_draw)
+
+
+def ngram(history: torch.Tensor, length: torch.Tensor, k: int, min_n: int, max_n: int,
+          earliest: bool = True) -> torch.Tensor:
+    """Prompt-lookup draft proposals ``[B, k]`` from the token history (see :func:`.reference.ngram`)."""
+    if history.is_cuda:
+        return require().ngram(history, length.to(torch.int32), int(k), int(min_n), int(max_n), bool(earliest))
+    return reference.ngram(history, length, k, min_n, max_n, earliest)

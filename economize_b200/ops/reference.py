@@ -13,6 +13,7 @@ import torch.nn.functional as F
 
 __all__ = [
     "attention",
+    "ngram",
     "rejection",
     "sample",
     "greedy_accept",
@@ -230,3 +231,26 @@ def rejection(p: torch.Tensor, q: torch.Tensor, drafts: torch.Tensor, u_acc: tor
         out[b, j] = max(tok, 0)
         n_acc[b] = j
     return n_acc, out
+
+
+def ngram(history: torch.Tensor, length: torch.Tensor, k: int, min_n: int, max_n: int,
+          earliest: bool = True) -> torch.Tensor:
+    """Prompt-lookup proposals ``[B, k]`` (see ``csrc/ngram.cu``): the ``k`` tokens after an earlier occurrence
+    of the history's last ``n`` tokens, longest ``n`` first; ``-1`` where there is none."""
+    batch = history.shape[0]
+    out = torch.full((batch, k), -1, dtype=torch.int64, device=history.device)
+    for b in range(batch):
+        n_hist = min(int(length[b]), history.shape[1])
+        h = history[b, :n_hist].tolist()
+        for n in range(max_n, min_n - 1, -1):
+            if n_hist <= n:
+                continue
+            pattern = h[n_hist - n:]
+            starts = [i for i in range(0, n_hist - n) if h[i:i + n] == pattern]
+            if starts:
+                i = starts[0] if earliest else starts[-1]
+                for j in range(k):
+                    if i + n + j < n_hist:
+                        out[b, j] = h[i + n + j]
+                break
+    return out

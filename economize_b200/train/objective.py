@@ -117,7 +117,60 @@ def default_objective(model) -> Objective:
     for tech in model.techniques.values():
         if Capability.DRAFTER in tech.capabilities and tech.name == "eagle3":
             return Eagle3TTT(model)
+        if tech.name == "medusa":
+            return MedusaCE(model)
         name = getattr(tech, "objective_name", None)
         if name is not None:
             return OBJECTIVES.get(name)(model)
     raise ConfigError("no attached technique has a default training objective")
+
+
+@OBJECTIVES.register("medusa_ce")
+class MedusaCE(Objective):
+    """Medusa-1 self-distillation: head ``j`` at position ``t`` learns the target's greedy token ``j + 1`` places
+    after the LM head's (cross-entropy, head ``j`` weighed ``decay**j``)."""
+
+    name = "medusa_ce"
+    defaults = OptimDefaults(lr=1e-3, warmup_steps=10)
+
+    def __init__(self, model, decay: float = 0.8) -> None:
+        super().__init__(model)
+        if "medusa" not in model.techniques:
+            raise ConfigError("medusa_ce needs an attached medusa technique")
+        self.tech = model.techniques["medusa"]
+        self.decay = decay
+
+    def parameters(self) -> list[torch.nn.Parameter]:
+        return [p for p in self.tech.parameters() if p.requires_grad]
+
+    def loss(self, tokens: torch.Tensor) -> tuple[torch.Tensor, dict[str, float]]:
+        import torch.nn.functional as F
+
+        tech = self.tech
+        key = -1 if tech.config.head == "own" else self.model.model.config.num_layers
+        aux, labels = teacher_pass(self.model, tokens, (key,))
+        states = aux[key].detach()
+        total, weight, metrics = 0.0, 0.0, {}
+        for j, head in enumerate(tech.heads):
+            x = states.to(head.blocks[0].linear.weight.dtype) if len(head.blocks) else states
+            for block in head.blocks:
+                x = x + F.silu(F.linear(x, block.linear.weight, block.linear.bias))
+            if head.proj is not None:
+                logits = F.linear(x, head.proj.weight).float()
+            else:
+                m = self.model.model
+                from ..ops.reference import rmsnorm
+
+                logits = F.linear(rmsnorm(x, m.norm, m.config.rms_norm_eps)[0], m.head_weight).float()
+            shift = j + 1
+            if labels.shape[1] <= shift:
+                break
+            target = labels[:, shift:]
+            ce = F.cross_entropy(logits[:, :-shift].reshape(-1, logits.shape[-1]), target.reshape(-1))
+            w = self.decay ** j
+            total = total + w * ce
+            weight += w
+            metrics[f"ce{j + 1}"] = float(ce.detach())
+        loss = total / max(weight, 1e-9)
+        metrics["loss"] = float(loss.detach())
+        return loss, metrics

@@ -79,3 +79,35 @@ def test_chain_is_bit_identical_to_plain(em, cuda):
         chain = em.decode_batch(prompts, 48, decoding=eco.DecodeConfig(cycle_length=5, cuda_graphs=graphs))
         for p, c in zip(plain, chain):
             assert torch.equal(p.tokens, c.tokens)
+
+
+@pytest.mark.parametrize("kind", ["lookup", "medusa", "draft_model"])
+def test_other_drafters_on_gpu(em, cuda, kind):
+    from economize_b200.techniques.draft_model import DraftModelConfig
+    from economize_b200.techniques.lookup import LookupConfig
+    from economize_b200.techniques.medusa import MedusaConfig
+
+    model = em.model
+    cfg = {"lookup": LookupConfig(), "medusa": MedusaConfig(num_heads=4, tree="mc_sim_7b_63"),
+           "draft_model": DraftModelConfig(model=model)}[kind]
+    e2 = eco.apply(model, cfg)
+    prompts = _prompts(cuda)
+    for graphs in (False, True):
+        dc = eco.DecodeConfig(cycle_length=5, cuda_graphs=graphs)
+        out = e2.decode_batch(prompts, 32, decoding=dc)
+        for p, r in zip(prompts, out):
+            assert r.tokens.numel() == 32
+            _assert_greedy(e2, p, r.tokens)
+    assert eco.ops.require().status(0) == 0
+
+
+def test_ngram_kernel(cuda):
+    from economize_b200.ops import reference
+
+    g = torch.Generator().manual_seed(3)
+    hist = torch.randint(0, 6, (8, 300), generator=g)
+    length = torch.randint(5, 300, (8,), generator=g).to(torch.int32)
+    for earliest in (True, False):
+        want = reference.ngram(hist, length, 5, 1, 3, earliest)
+        got = eco.ops.ngram(hist.to(cuda), length.to(cuda), 5, 1, 3, earliest)
+        assert torch.equal(got.cpu(), want)
