@@ -226,8 +226,7 @@ class SpecEngine:
             hidden, aux = model.forward_step(prompts, StepBatch.prefill(lengths, width), st.cache, capture)
         last_idx = (lengths.long() - 1).clamp_min(0)
         rows = torch.arange(batch, device=prompts.device)
-        logits = model.logits(hidden[rows, last_idx])
-        bonus = self._choose(logits)
+        bonus = self._pred(hidden[rows, last_idx])
         st.kv_len.copy_(lengths)
         st.last.copy_(bonus)
         st.history.zero_()
@@ -318,7 +317,7 @@ class SpecEngine:
         sb = StepBatch(st.kv_len, one, st.kv_len[:, None].contiguous(),
                        torch.ones(batch, 1, dtype=torch.int64, device=st.kv_len.device))
         hidden, _ = model.forward_step(st.last[:, None], sb, st.cache)
-        pred = self._choose(model.logits(hidden[:, 0]))
+        pred = self._pred(hidden[:, 0])
         active = st.n_out < st.max_new
         st.out.scatter_(1, torch.where(active, st.n_out, st.out_cap).long()[:, None], pred[:, None])
         st.n_out.add_(1)
@@ -346,8 +345,7 @@ class SpecEngine:
         n_new = torch.full((batch,), length, dtype=torch.int32, device=dev)
         sb = StepBatch(st.kv_len, n_new, positions, bits)
         hidden, aux = model.forward_step(tokens.clamp_min(0), sb, st.cache, drafter.capture_layers)
-        logits = model.logits(hidden)  # [B, T, V]
-        n_acc, path, out = self._verify(tokens, parents, logits, draft_tokens, q_full)
+        n_acc, path, out = self._verify(tokens, parents, hidden, draft_tokens, q_full)
         ops.kv_compact(st.cache.data, st.kv_len, path, n_acc)
         # ---- commit ----
         active = st.n_out < st.max_new
@@ -438,10 +436,19 @@ class SpecEngine:
         u = torch.rand(probs.shape[:-1], device=probs.device)
         return ops.sample(probs.contiguous(), u)
 
-    def _verify(self, tokens: torch.Tensor, parents: torch.Tensor, logits: torch.Tensor, drafts: torch.Tensor,
+    def _pred(self, hidden: torch.Tensor) -> torch.Tensor:
+        """The exact token after every row of final hidden states: greedy through the model's (possibly
+        vocabulary-parallel) argmax, or a draw from the selector over the full logits."""
+        if self.selector is None:
+            return self.model.greedy(hidden)
+        return self._choose(self.model.logits(hidden))
+
+    def _verify(self, tokens: torch.Tensor, parents: torch.Tensor, hidden: torch.Tensor, drafts: torch.Tensor,
                 q_full: torch.Tensor | None) -> tuple[torch.Tensor, torch.Tensor, torch.Tensor]:
         batch, length = tokens.shape
         dev = tokens.device
+        plain_greedy = self.selector is None and not isinstance(self.verifier, TypicalVerifier)
+        logits = None if plain_greedy else self.model.logits(hidden)  # [B, T, V]
         if self.rejection:
             p = self.selector.probs(logits).contiguous()  # [B, k + 1, V]
             k = drafts.shape[1]
@@ -453,7 +460,7 @@ class SpecEngine:
             path = torch.arange(length, device=dev, dtype=torch.int32).expand(batch, length)
             path = torch.minimum(path, n_acc[:, None]).contiguous()
             return n_acc, path, out
-        pred = self._choose(logits)  # [B, T]
+        pred = self.model.greedy(hidden) if plain_greedy else self._choose(logits)  # [B, T]
         if self.accept_all:
             pred = torch.cat([drafts.clamp_min(0), pred[:, -1:]], 1)
             return ops.greedy_accept(tokens, parents, pred)

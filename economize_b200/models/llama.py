@@ -75,6 +75,10 @@ class CausalLM(nn.Module):
         self.lm_head = None if config.tie_word_embeddings else nn.Parameter(
             torch.empty(config.vocab_size, config.hidden_size, **kw))
         self._rope: tuple[torch.Tensor, torch.Tensor] | None = None
+        #: tensor-parallel group (set by economize_b200.parallel.tp.shard_model) and this rank's shard sizes
+        self.tp = None
+        self.local = dict(num_heads=config.num_heads, num_kv_heads=config.num_kv_heads,
+                          intermediate_size=config.intermediate_size, vocab_offset=0, vocab_size=config.vocab_size)
 
     # ---- properties --------------------------------------------------------------------------------------------
     @property
@@ -102,7 +106,12 @@ class CausalLM(nn.Module):
 
     def new_cache(self, batch: int, capacity: int) -> KVCache:
         c = self.config
-        return KVCache(c.num_layers, batch, c.num_kv_heads, capacity, c.head_dim, self.dtype, self.device)
+        return KVCache(c.num_layers, batch, self.local["num_kv_heads"], capacity, c.head_dim, self.dtype,
+                       self.device)
+
+    @property
+    def tp_size(self) -> int:
+        return 1 if self.tp is None else self.tp.size
 
     # ---- forward -----------------------------------------------------------------------------------------------
     def embed_tokens(self, tokens: torch.Tensor) -> torch.Tensor:
@@ -125,9 +134,9 @@ class CausalLM(nn.Module):
             x, resid = ops.rmsnorm(h, layer.attn_norm, c.rms_norm_eps, resid)
             if i in capture:
                 aux[i] = resid
-            h = self._attention(layer, i, x, batch, cache, cos, sin)
+            h = self._reduce(self._attention(layer, i, x, batch, cache, cos, sin))
             x, resid = ops.rmsnorm(h, layer.mlp_norm, c.rms_norm_eps, resid)
-            h = self._mlp(layer, x)
+            h = self._reduce(self._mlp(layer, x))
         out, resid = ops.rmsnorm(h, self.norm, c.rms_norm_eps, resid)
         if c.num_layers in capture:
             aux[c.num_layers] = resid
@@ -135,12 +144,17 @@ class CausalLM(nn.Module):
             aux[-1] = out
         return out, aux
 
+    def _reduce(self, partial: torch.Tensor) -> torch.Tensor:
+        """Sum a row-parallel projection's partial outputs over the tensor-parallel ranks."""
+        return partial if self.tp is None or self.tp.size == 1 else self.tp.all_reduce(partial)
+
     def _attention(self, layer: DecoderLayer, index: int, x: torch.Tensor, batch: StepBatch, cache: KVCache,
                    cos: torch.Tensor, sin: torch.Tensor) -> torch.Tensor:
         c = self.config
         qkv = ops.linear(x, layer.wqkv, layer.bqkv)
         k_cache, v_cache = cache.layer(index)
-        q = ops.rope_store(qkv, batch.positions, cos, sin, c.num_heads, c.num_kv_heads, c.head_dim, k_cache,
+        q = ops.rope_store(qkv, batch.positions, cos, sin, self.local["num_heads"], self.local["num_kv_heads"],
+                           c.head_dim, k_cache,
                            v_cache, batch.kv_len, batch.n_new, layer.q_norm, layer.k_norm, c.rms_norm_eps,
                            q_offset=batch.q_offset)
         o = ops.attention(q, k_cache, v_cache, batch.kv_len, batch.n_new, batch.mask, q_offset=batch.q_offset)
@@ -154,7 +168,22 @@ class CausalLM(nn.Module):
         return ops.linear(ops.silu_mul(ops.linear(x, layer.w_gate_up)), layer.w_down)
 
     def logits(self, hidden: torch.Tensor) -> torch.Tensor:
-        return ops.linear(hidden, self.head_weight)
+        """Logits over the full vocabulary (gathered from the vocabulary shards under tensor parallelism)."""
+        local = ops.linear(hidden, self.head_weight)
+        if self.tp is None or self.tp.size == 1:
+            return local
+        every = self.tp.all_gather(local)  # [P, ..., V/P]
+        return torch.cat(list(every.unbind(0)), -1)
+
+    def greedy(self, hidden: torch.Tensor) -> torch.Tensor:
+        """Argmax token after every row of ``hidden`` (distributed over vocabulary shards under TP, without
+        gathering the logits)."""
+        local = ops.linear(hidden, self.head_weight)
+        if self.tp is None or self.tp.size == 1:
+            return ops.argmax(local)
+        from ..parallel.tp import tp_argmax
+
+        return tp_argmax(local, self.tp, self.local["vocab_offset"])
 
     # ---- Hugging Face interop ----------------------------------------------------------------------------------
     @classmethod
