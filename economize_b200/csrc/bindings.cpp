@@ -9,6 +9,7 @@
 
 #include <cstring>
 #include <list>
+#include <string>
 #include <mutex>
 #include <tuple>
 #include <unordered_map>
@@ -353,6 +354,69 @@ Tensor ngram(Tensor history, Tensor len, int64_t k, int64_t min_n, int64_t max_n
   return drafts;
 }
 
+// ---- symmetric memory over CUDA IPC -------------------------------------------------------------------------
+// symm_alloc(bytes) -> (device pointer, IPC handle bytes); symm_open(handle) -> peer pointer; symm_free(ptr).
+std::tuple<int64_t, py::bytes> symm_alloc(int64_t bytes) {
+  void* ptr = nullptr;
+  TORCH_CHECK(cudaMalloc(&ptr, bytes) == cudaSuccess, "symm_alloc: cudaMalloc failed");
+  TORCH_CHECK(cudaMemset(ptr, 0, bytes) == cudaSuccess, "symm_alloc: cudaMemset failed");
+  cudaIpcMemHandle_t handle;
+  TORCH_CHECK(cudaIpcGetMemHandle(&handle, ptr) == cudaSuccess, "symm_alloc: cudaIpcGetMemHandle failed");
+  return {reinterpret_cast<int64_t>(ptr), py::bytes(reinterpret_cast<const char*>(&handle), sizeof(handle))};
+}
+
+int64_t symm_open(py::bytes handle_bytes) {
+  std::string raw = handle_bytes;
+  TORCH_CHECK(raw.size() == sizeof(cudaIpcMemHandle_t), "symm_open: bad handle");
+  cudaIpcMemHandle_t handle;
+  std::memcpy(&handle, raw.data(), sizeof(handle));
+  void* ptr = nullptr;
+  const cudaError_t err = cudaIpcOpenMemHandle(&ptr, handle, cudaIpcMemLazyEnablePeerAccess);
+  TORCH_CHECK(err == cudaSuccess, "symm_open: cudaIpcOpenMemHandle failed: ", cudaGetErrorString(err));
+  return reinterpret_cast<int64_t>(ptr);
+}
+
+void symm_close(int64_t ptr) { cudaIpcCloseMemHandle(reinterpret_cast<void*>(ptr)); }
+void symm_free(int64_t ptr) { cudaFree(reinterpret_cast<void*>(ptr)); }
+int64_t symm_control_bytes() { return static_cast<int64_t>(ecz::symm_control_bytes()); }
+
+ecz::PeerPtrs peer_ptrs(const std::vector<int64_t>& ptrs) {
+  TORCH_CHECK(ptrs.size() <= static_cast<size_t>(ecz::kMaxPeers), "at most 8 peers");
+  ecz::PeerPtrs p{};
+  for (size_t i = 0; i < ptrs.size(); ++i) p.ptr[i] = reinterpret_cast<void*>(ptrs[i]);
+  return p;
+}
+
+void push(Tensor src, std::vector<int64_t> ptrs, int64_t rank, int64_t parity, int64_t slot_elems) {
+  CHECK_CUDA(src);
+  CHECK_BF16(src);
+  c10::cuda::CUDAGuard guard(src.device());
+  src = src.contiguous();
+  const int rc = ecz::launch_push(src.data_ptr(), src.numel(), peer_ptrs(ptrs), static_cast<int>(rank),
+                                  static_cast<int>(ptrs.size()), static_cast<int>(parity), slot_elems,
+                                  num_sms(src.get_device()), at::cuda::getCurrentCUDAStream());
+  TORCH_CHECK(rc == 0, "push: size must be a multiple of 8 and fit the slot");
+}
+
+std::tuple<Tensor, Tensor> reduce_rmsnorm(std::vector<int64_t> ptrs, int64_t rank, int64_t parity, int64_t slot_elems,
+                                          c10::optional<Tensor> resid, Tensor w, double eps, int64_t rows,
+                                          int64_t hidden, Tensor like) {
+  CHECK_CUDA(w);
+  c10::cuda::CUDAGuard guard(w.device());
+  auto out = at::empty({rows, hidden}, like.options());
+  auto resid_out = at::empty({rows, hidden}, like.options());
+  Tensor r;
+  if (resid.has_value()) r = resid->contiguous();
+  const int rc = ecz::launch_reduce_rmsnorm(peer_ptrs(ptrs), static_cast<int>(rank), static_cast<int>(ptrs.size()),
+                                            static_cast<int>(parity), slot_elems,
+                                            resid.has_value() ? r.data_ptr() : nullptr, w.data_ptr(), out.data_ptr(),
+                                            resid_out.data_ptr(), static_cast<int>(rows), static_cast<int>(hidden),
+                                            static_cast<float>(eps), status_word(w.device()),
+                                            at::cuda::getCurrentCUDAStream());
+  TORCH_CHECK(rc == 0, "reduce_rmsnorm: rows x hidden must fit the slot, hidden a multiple of 8");
+  return {out, resid_out};
+}
+
 int64_t status(int64_t device) {
   const at::Device dev(at::kCUDA, static_cast<c10::DeviceIndex>(device));
   c10::cuda::CUDAGuard guard(dev);
@@ -389,6 +453,13 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("sample", &sample, "inverse-CDF draw of one token per probability row");
   m.def("rejection", &rejection, "lossless speculative sampling of a draft chain (accept/reject + resample)");
   m.def("ngram", &ngram, "prompt-lookup draft proposals from the token history");
+  m.def("symm_alloc", &symm_alloc, "cudaMalloc an IPC-exportable buffer: (pointer, handle)");
+  m.def("symm_open", &symm_open, "map a peer's buffer from its IPC handle");
+  m.def("symm_close", &symm_close, "unmap a peer's buffer");
+  m.def("symm_free", &symm_free, "free an own symmetric buffer");
+  m.def("symm_control_bytes", &symm_control_bytes, "bytes of the control block before the data slots");
+  m.def("push", &push, "store this rank's partial into every peer's slot and signal arrival");
+  m.def("reduce_rmsnorm", &reduce_rmsnorm, "wait for every rank's partial, sum, add residual, RMSNorm");
   m.def("status", &status, "read and clear the device status word of bounded waits");
   m.def("attention_plan", &attention_plan, "(m_tiles, splits, chunks_per_split) of an attention launch");
   m.def("gemm_splits", &gemm_splits, "split-K factor of a GEMM launch");

@@ -7,6 +7,11 @@
 
 namespace ecz {
 
+constexpr int kMaxPeers = 8;
+struct PeerPtrs {
+  void* ptr[kMaxPeers];
+};
+
 struct AttnPlan {
   int m_tiles = 1;
   int splits = 1;
@@ -61,6 +66,14 @@ int launch_rejection(const float* p, const float* q, const int64_t* drafts, cons
 // ngram.cu
 int launch_ngram(const int64_t* history, const int* len, int64_t* drafts, int B, int cap, int k, int min_n, int max_n,
                  bool earliest, cudaStream_t stream);
+
+// comm.cu: fused NVLink all-reduce (+ residual add + RMSNorm) on IPC-mapped symmetric buffers
+size_t symm_control_bytes();
+int launch_push(const void* src, long elems, const PeerPtrs& peers, int rank, int world, int parity, long slot_elems,
+                int num_sms, cudaStream_t stream);
+int launch_reduce_rmsnorm(const PeerPtrs& peers, int rank, int world, int parity, long slot_elems, const void* resid,
+                          const void* w, void* out, void* resid_out, int rows, int hidden, float eps,
+                          unsigned* status, cudaStream_t stream);
 
 // tmap.cpp: a 2-D bf16 tensor map over a row-major [rows, cols] matrix with a {64, box_rows} box and the 128-byte
 // swizzle (cols * 2 bytes must be a multiple of 16). Returns 0 on success.

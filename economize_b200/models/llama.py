@@ -129,24 +129,34 @@ class CausalLM(nn.Module):
         resid: torch.Tensor | None = None
         aux: dict[int, torch.Tensor] = {}
         todo = layers if layers is not None else range(c.num_layers)
+        partial = False  # h is a row-parallel partial awaiting its all-reduce (tensor parallelism)
         for i in todo:
             layer = self.layers[i]
-            x, resid = ops.rmsnorm(h, layer.attn_norm, c.rms_norm_eps, resid)
+            x, resid = self._norm(h, layer.attn_norm, resid, partial)
             if i in capture:
                 aux[i] = resid
-            h = self._reduce(self._attention(layer, i, x, batch, cache, cos, sin))
-            x, resid = ops.rmsnorm(h, layer.mlp_norm, c.rms_norm_eps, resid)
-            h = self._reduce(self._mlp(layer, x))
-        out, resid = ops.rmsnorm(h, self.norm, c.rms_norm_eps, resid)
+            h = self._attention(layer, i, x, batch, cache, cos, sin)
+            x, resid = self._norm(h, layer.mlp_norm, resid, True)
+            h = self._mlp(layer, x)
+            partial = True
+        out, resid = self._norm(h, self.norm, resid, partial)
         if c.num_layers in capture:
             aux[c.num_layers] = resid
         if -1 in capture:  # the final-normed hidden states (what the LM head reads)
             aux[-1] = out
         return out, aux
 
-    def _reduce(self, partial: torch.Tensor) -> torch.Tensor:
-        """Sum a row-parallel projection's partial outputs over the tensor-parallel ranks."""
-        return partial if self.tp is None or self.tp.size == 1 else self.tp.all_reduce(partial)
+    def _norm(self, h: torch.Tensor, weight: torch.Tensor, resid: torch.Tensor | None,
+              partial: bool) -> tuple[torch.Tensor, torch.Tensor]:
+        """Residual add + RMSNorm; under tensor parallelism a row-parallel partial ``h`` is first summed over the
+        ranks (NCCL, or the fused NVLink push/reduce kernels that also do the add and the norm)."""
+        eps = self.config.rms_norm_eps
+        tp = self.tp
+        if not partial or tp is None or tp.size == 1:
+            return ops.rmsnorm(h, weight, eps, resid)
+        if tp.fused and tp.comm is not None and tp.comm.fits(h.numel() // h.shape[-1]):
+            return tp.comm.reduce_rmsnorm(h, weight, eps, resid)
+        return ops.rmsnorm(tp.all_reduce(h), weight, eps, resid)
 
     def _attention(self, layer: DecoderLayer, index: int, x: torch.Tensor, batch: StepBatch, cache: KVCache,
                    cos: torch.Tensor, sin: torch.Tensor) -> torch.Tensor:
