@@ -48,6 +48,10 @@ def parse() -> argparse.Namespace:
     p.add_argument("--impl", choices=("ours", "reference"), default="ours")
     p.add_argument("--model", choices=("llama31_8b", "tiny"), default="llama31_8b")
     p.add_argument("--no-graphs", action="store_true")
+    p.add_argument("--parallel", choices=("dp", "tp"), default="dp",
+                   help="dp: one replica per GPU; tp: one model sharded over all GPUs (fused NVLink collectives)")
+    p.add_argument("--nccl-tp", action="store_true", help="with --parallel tp: NCCL all-reduces instead of the fused "
+                   "GEMM->push / reduce+RMSNorm kernels")
     return p.parse_args()
 
 
@@ -104,7 +108,7 @@ def setup_dist(args: argparse.Namespace):
 
         import torch.distributed as dist
 
-        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300),
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=1800),
                                 device_id=torch.device("cuda", local))
     return world, rank, local
 
@@ -315,8 +319,37 @@ def count_launches(step) -> int:
 def run_ours(args, world, rank):
     target = build_target(args)
     vocab = target.config.vocab_size
+    if args.parallel == "tp" and world > 1:
+        return run_ours_tp(args, world, rank, target)
     prompts = prompts_for(args, rank, vocab, "cuda")
     em, _ = build_drafter(target, args, rank, world, prompts)
+    cfg = decode_config(args)
+    rows = list(prompts)
+    results = {"cfg": cfg}
+
+    def step():
+        results["r"] = em.decode_batch(rows, args.new_tokens, decoding=cfg)
+
+    return em, step, results, prompts
+
+
+def run_ours_tp(args, world, rank, target):
+    """One request stream served by all ranks: the target sharded over them, the drafter replicated."""
+    import torch.distributed as dist
+
+    from economize_b200.distributed import TPGroup, tensor_parallel
+
+    prompts = prompts_for(args, 0, target.config.vocab_size, "cuda")  # the same stream on every rank
+    if rank == 0:
+        em, state = build_drafter(target, args, 0, 1, prompts)
+    dist.barrier()
+    if rank != 0:
+        em, state = build_drafter(target, args, 0, 1, prompts)  # loads rank 0's cached weights
+    tech = em.techniques["eagle3"]
+    # bit-identical drafters on every rank (every rank must draft the same tree)
+    for tensor in tech.state_dict().values():
+        dist.broadcast(tensor, src=0)
+    tensor_parallel(em, TPGroup(rank, world), fused=not args.nccl_tp)
     cfg = decode_config(args)
     rows = list(prompts)
     results = {"cfg": cfg}
@@ -331,6 +364,9 @@ def run_reference(args, world, rank):
     ref = reference_module()
     if ref is None:
         return None, "reference not importable from baseline/_ref"
+    if args.parallel == "tp" and world > 1:
+        return None, ("the reference's tensor parallelism loads a checkpoint from disk with transformers' "
+                      "tp_plan='auto'; this benchmark's random-init weights exist only in memory")
     from economize.techniques.eagle3 import Eagle3Config as RefEagle3Config
 
     target = build_target(args)
@@ -388,7 +424,8 @@ def main() -> None:
         barrier(world)
     ms = start.elapsed_time(end) / args.steps
     ms_max = reduce_max(ms, world)
-    new_tokens = args.batch * args.new_tokens * world
+    streams = 1 if (args.parallel == "tp" and world > 1) else world
+    new_tokens = args.batch * args.new_tokens * streams
     value = new_tokens / (ms_max / 1e3)
     accepted, cycles = acceptance(results["r"])
     tau_local = 1.0 + accepted / cycles if cycles else None
@@ -420,7 +457,8 @@ def main() -> None:
     if rank == 0:
         line = {
             "metric": METRIC, "value": round(value, 2), "unit": "tok/s", "n_gpus": world, "steps": args.steps,
-            "warmup": args.warmup, "ms_per_step": round(ms_max, 3), "higher_is_better": True, "scaling": "weak",
+            "warmup": args.warmup, "ms_per_step": round(ms_max, 3), "higher_is_better": True,
+            "scaling": "strong" if (args.parallel == "tp" and world > 1) else "weak",
             "vs_baseline": (value / BASELINE_TOKS) if BASELINE_TOKS else None, "dtype": "bf16",
             "data": "synthetic (uniform-random prompts, random-init weights)",
             "mean_accepted_len": round(tau, 4) if tau is not None else None,
@@ -429,22 +467,38 @@ def main() -> None:
                                   f"{args.train_steps} steps in {args.train_rounds} rounds on the greedy and "
                                   "speculative trajectories of both implementations on the benchmark prompts (same "
                                   "weights in both arms)",
-                       "global_batch": args.batch * world, "seq_len": args.prompt_len,
-                       "new_tokens": args.new_tokens, "parallelism": f"dp{world}",
+                       "global_batch": args.batch * streams, "seq_len": args.prompt_len,
+                       "new_tokens": args.new_tokens,
+                       "parallelism": (f"tp{world}" + ("-nccl" if args.nccl_tp else "-fused"))
+                       if (args.parallel == "tp" and world > 1) else f"dp{world}",
                        "train_steps": args.train_steps, "cuda_graphs": not args.no_graphs,
                        "l2": "weights (16 GB) exceed L2; no flush"},
             "clocks": clocks.summary(),
             "e2e": {"value": round(new_tokens / (e2e_ms / 1e3), 2), "unit": "tok/s",
-                    "h2d_bytes_per_step": sum(p.numel() * p.element_size() for p in host_prompts) * world,
-                    "d2h_bytes_per_step": sum(t.numel() * t.element_size() for t in toks) * world},
+                    "h2d_bytes_per_step": sum(p.numel() * p.element_size() for p in host_prompts) * streams,
+                    "d2h_bytes_per_step": sum(t.numel() * t.element_size() for t in toks) * streams},
             "gpu_launches": launches,
         }
         if args.impl == "reference":
             line["impl"] = "reference"
         print(json.dumps(line))
+    # release the captured graphs (they may hold NCCL calls) and the NVLink buffers before the group goes away
+    engine_model = getattr(model, "model", None)
+    if hasattr(model, "refresh"):
+        model.refresh()
+    tp = getattr(engine_model, "tp", None)
+    if tp is not None and getattr(tp, "comm", None) is not None:
+        tp.comm.close()
+    results.clear()
+    del step, model
+    import gc
+
+    gc.collect()
+    torch.cuda.synchronize()
     if world > 1:
         import torch.distributed as dist
 
+        dist.barrier()
         dist.destroy_process_group()
 
 

@@ -387,6 +387,37 @@ ecz::PeerPtrs peer_ptrs(const std::vector<int64_t>& ptrs) {
   return p;
 }
 
+// Row-parallel GEMM whose output tiles go straight into every peer's slot (tensor-parallel push mode).
+void linear_push(Tensor x, Tensor w, std::vector<int64_t> ptrs, int64_t rank, int64_t parity, int64_t slot_elems) {
+  CHECK_CUDA(x);
+  CHECK_BF16(x);
+  CHECK_BF16(w);
+  TORCH_CHECK(x.dim() == 2 && w.dim() == 2 && x.size(1) == w.size(1), "linear_push expects x [M, K] and w [N, K]");
+  c10::cuda::CUDAGuard guard(x.device());
+  x = x.contiguous();
+  w = w.contiguous();
+  const int M = static_cast<int>(x.size(0)), K = static_cast<int>(x.size(1)), N = static_cast<int>(w.size(0));
+  TORCH_CHECK(static_cast<long>(M) * N <= slot_elems, "linear_push: output larger than the slot");
+  const int sms = num_sms(x.get_device());
+  const int splits = ecz::gemm_splits(M, N, K, sms);
+  Tensor ws;
+  if (splits > 1) ws = at::empty({static_cast<int64_t>(splits) * M * N}, x.options().dtype(at::kFloat));
+  ecz::PeerOut peer{};
+  peer.ptrs = peer_ptrs(ptrs);
+  peer.world = static_cast<int>(ptrs.size());
+  peer.rank = static_cast<int>(rank);
+  peer.parity = static_cast<int>(parity);
+  peer.slot_elems = slot_elems;
+  peer.control_bytes = static_cast<long>(ecz::symm_control_bytes());
+  const CUtensorMap* tw = tensor_map(w.data_ptr(), N, K, K, 128);
+  const CUtensorMap* tx = tensor_map(x.data_ptr(), M, K, K, ecz::gemm_block_n(M));
+  cudaStream_t stream = at::cuda::getCurrentCUDAStream();
+  const int rc = ecz::launch_gemm_bf16(tw, tx, nullptr, splits > 1 ? ws.data_ptr<float>() : nullptr, M, N, K, splits,
+                                       status_word(x.device()), stream,
+                                       splits > 1 ? split_counters(x.device(), stream) : nullptr, &peer);
+  TORCH_CHECK(rc == 0, "linear_push: unsupported shape");
+}
+
 void push(Tensor src, std::vector<int64_t> ptrs, int64_t rank, int64_t parity, int64_t slot_elems) {
   CHECK_CUDA(src);
   CHECK_BF16(src);
@@ -459,6 +490,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("symm_free", &symm_free, "free an own symmetric buffer");
   m.def("symm_control_bytes", &symm_control_bytes, "bytes of the control block before the data slots");
   m.def("push", &push, "store this rank's partial into every peer's slot and signal arrival");
+  m.def("linear_push", &linear_push, "row-parallel GEMM whose output tiles go into every peer's slot");
   m.def("reduce_rmsnorm", &reduce_rmsnorm, "wait for every rank's partial, sum, add residual, RMSNorm");
   m.def("status", &status, "read and clear the device status word of bounded waits");
   m.def("attention_plan", &attention_plan, "(m_tiles, splits, chunks_per_split) of an attention launch");

@@ -46,9 +46,9 @@ __global__ void __launch_bounds__(256) push_kernel(const bf16* __restrict__ src,
       dst[v] = reinterpret_cast<const uint4*>(src)[v];
     }
   }
-  __threadfence_system();
-  __syncthreads();
+  __syncthreads();  // the CTA's stores are ordered before thread 0's system-scope fence and signal
   if (threadIdx.x == 0) {
+    __threadfence_system();
     Control* own = static_cast<Control*>(peers.ptr[rank]);
     const unsigned done = atomicAdd(&own->push_done, 1u);
     if (done == gridDim.x - 1) {  // the last CTA of this push announces it to every rank

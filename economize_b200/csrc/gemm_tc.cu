@@ -33,11 +33,35 @@ struct GemmCfg {
   static constexpr int kSmem = kStages * kStageBytes + 1024 /*align*/ + 256 /*barriers*/;
 };
 
+// Push mode (tensor-parallel row-parallel projections): output tiles go straight into slot `rank` of every peer's
+// receive buffer (bf16 [rows, N], parity `parity`), and the last tile writer of the grid announces the arrival to
+// every peer, as the push kernel of comm.cu does.
+__device__ __forceinline__ bf16* peer_slot(const PeerOut& peer, int p) {
+  return reinterpret_cast<bf16*>(static_cast<uint8_t*>(peer.ptrs.ptr[p]) + peer.control_bytes) +
+         (static_cast<long>(peer.parity) * peer.world + peer.rank) * peer.slot_elems;
+}
+
+__device__ __forceinline__ void push_signal(const PeerOut& peer, bool wrote, unsigned writers_total) {
+  // every CTA that stored a tile counts itself; the last one signals the peers (writers_total = tiles). The CTA
+  // barrier orders all threads' stores before thread 0's system-scope fence.
+  __syncthreads();
+  if (threadIdx.x == 0 && wrote) {
+    __threadfence_system();
+    unsigned* own = reinterpret_cast<unsigned*>(peer.ptrs.ptr[peer.rank]);
+    const unsigned done = atomicAdd(own + 4, 1u);  // push_done of the control block
+    if (done == writers_total - 1) {
+      own[4] = 0;
+      __threadfence_system();
+      for (int p = 0; p < peer.world; ++p) atomicAdd_system(static_cast<unsigned*>(peer.ptrs.ptr[p]) + peer.parity, 1u);
+    }
+  }
+}
+
 template <int BN>
 __global__ void __launch_bounds__(128, 1)
     gemm_swapab_kernel(const __grid_constant__ CUtensorMap tm_w, const __grid_constant__ CUtensorMap tm_x,
                        bf16* __restrict__ y, float* __restrict__ ws, int* __restrict__ counters, int M, int N,
-                       int K, int kb_per_split, unsigned* status) {
+                       int K, int kb_per_split, unsigned* status, PeerOut peer) {
   using Cfg = GemmCfg<BN>;
   constexpr int S = Cfg::kStages;
   extern __shared__ uint8_t smem_raw[];
@@ -134,7 +158,14 @@ __global__ void __launch_bounds__(128, 1)
 #pragma unroll
           for (int j = 0; j < 16; ++j) {
             const int m = m0 + c + j;
-            if (m < M) y[static_cast<size_t>(m) * N + n] = __float2bfloat16(v[j]);
+            if (m < M) {
+              const bf16 o = __float2bfloat16(v[j]);
+              if (peer.world == 0) {
+                y[static_cast<size_t>(m) * N + n] = o;
+              } else {
+                for (int p = 0; p < peer.world; ++p) peer_slot(peer, p)[static_cast<size_t>(m) * N + n] = o;
+              }
+            }
           }
         } else {
           float* part = ws + static_cast<size_t>(split) * M * N;
@@ -150,6 +181,7 @@ __global__ void __launch_bounds__(128, 1)
   tc_fence_before();
   __syncthreads();
   if (warp == 0) tmem_dealloc(tmem, Cfg::kTmemCols);
+  bool wrote = ok && ws == nullptr;  // this CTA stored its output tile (split-K: only the tile's last CTA does)
   if (ok && ws != nullptr && counters != nullptr) {
     // In-kernel split-K reduction: the last CTA of this output tile (counted with a self-resetting atomic) sums
     // the partials of all splits in split order, so the result does not depend on which CTA finishes last.
@@ -194,14 +226,21 @@ __global__ void __launch_bounds__(128, 1)
               uint2 packed;
               packed.x = *reinterpret_cast<uint32_t*>(&lo);
               packed.y = *reinterpret_cast<uint32_t*>(&hi);
-              *reinterpret_cast<uint2*>(y + static_cast<size_t>(m) * N + col) = packed;
+              if (peer.world == 0) {
+                *reinterpret_cast<uint2*>(y + static_cast<size_t>(m) * N + col) = packed;
+              } else {
+                for (int p = 0; p < peer.world; ++p)
+                  *reinterpret_cast<uint2*>(peer_slot(peer, p) + static_cast<size_t>(m) * N + col) = packed;
+              }
             }
           }
         }
       }
       if (threadIdx.x == 0) counters[tile] = 0;
     }
+    wrote = last;
   }
+  if (peer.world > 0 && ok) push_signal(peer, wrote, gridDim.x * gridDim.y);
 }
 
 __global__ void __launch_bounds__(256) splitk_reduce_kernel(const float* __restrict__ ws, bf16* __restrict__ y,
@@ -226,7 +265,7 @@ __global__ void __launch_bounds__(256) splitk_reduce_kernel(const float* __restr
 
 template <int BN>
 int run_gemm(const CUtensorMap& tm_w, const CUtensorMap& tm_x, void* y, float* ws, int* counters, int M, int N,
-             int K, int splits, unsigned* status, cudaStream_t stream) {
+             int K, int splits, unsigned* status, cudaStream_t stream, const PeerOut& peer) {
   using Cfg = GemmCfg<BN>;
   static bool configured = false;
   if (!configured) {
@@ -238,7 +277,7 @@ int run_gemm(const CUtensorMap& tm_w, const CUtensorMap& tm_x, void* y, float* w
   splits = (total_kb + kbps - 1) / kbps;  // no empty split
   dim3 grid((N + kBM - 1) / kBM, (M + BN - 1) / BN, splits);
   launch_pdl(gemm_swapab_kernel<BN>, grid, dim3(128), Cfg::kSmem, stream, tm_w, tm_x, static_cast<bf16*>(y),
-             splits > 1 ? ws : nullptr, splits > 1 ? counters : nullptr, M, N, K, kbps, status);
+             splits > 1 ? ws : nullptr, splits > 1 ? counters : nullptr, M, N, K, kbps, status, peer);
   if (splits > 1 && counters == nullptr) {
     const long total = static_cast<long>(M) * N;
     const int blocks = static_cast<int>(std::min<long>((total / 4 + 255) / 256, 148L * 8));
@@ -530,13 +569,16 @@ int launch_gemm_persistent(const CUtensorMap* tm_w, const CUtensorMap* tm_x, voi
 }
 
 int launch_gemm_bf16(const CUtensorMap* tm_w, const CUtensorMap* tm_x, void* y, float* ws, int M, int N, int K,
-                     int splits, unsigned* status, cudaStream_t stream, int* counters) {
+                     int splits, unsigned* status, cudaStream_t stream, int* counters, const PeerOut* peer) {
   if (K % 8 != 0 || N % 4 != 0) return -1;
+  if (splits > 1 && counters == nullptr && peer != nullptr && peer->world > 0) return -1;  // push needs the fused reduce
+  const PeerOut none{};
+  const PeerOut& pe = peer != nullptr ? *peer : none;
   switch (gemm_block_n(M)) {
-    case 32: return run_gemm<32>(*tm_w, *tm_x, y, ws, counters, M, N, K, splits, status, stream);
-    case 64: return run_gemm<64>(*tm_w, *tm_x, y, ws, counters, M, N, K, splits, status, stream);
-    case 128: return run_gemm<128>(*tm_w, *tm_x, y, ws, counters, M, N, K, splits, status, stream);
-    default: return run_gemm<256>(*tm_w, *tm_x, y, ws, counters, M, N, K, splits, status, stream);
+    case 32: return run_gemm<32>(*tm_w, *tm_x, y, ws, counters, M, N, K, splits, status, stream, pe);
+    case 64: return run_gemm<64>(*tm_w, *tm_x, y, ws, counters, M, N, K, splits, status, stream, pe);
+    case 128: return run_gemm<128>(*tm_w, *tm_x, y, ws, counters, M, N, K, splits, status, stream, pe);
+    default: return run_gemm<256>(*tm_w, *tm_x, y, ws, counters, M, N, K, splits, status, stream, pe);
   }
 }
 

@@ -12,6 +12,16 @@ struct PeerPtrs {
   void* ptr[kMaxPeers];
 };
 
+// Where a row-parallel GEMM pushes its output in tensor-parallel push mode (world == 0: ordinary output).
+struct PeerOut {
+  PeerPtrs ptrs;
+  int world = 0;
+  int rank = 0;
+  int parity = 0;
+  long slot_elems = 0;
+  long control_bytes = 256;
+};
+
 struct AttnPlan {
   int m_tiles = 1;
   int splits = 1;
@@ -42,7 +52,8 @@ int gemm_splits(int M, int N, int K, int num_sms);
 // With `counters` (a zeroed int array of at least num_sms entries, private to the stream) the split-K partials are
 // reduced inside the GEMM by the last CTA of each tile; without, by a second kernel.
 int launch_gemm_bf16(const CUtensorMap* tm_w, const CUtensorMap* tm_x, void* y, float* ws, int M, int N, int K,
-                     int splits, unsigned* status, cudaStream_t stream, int* counters = nullptr);
+                     int splits, unsigned* status, cudaStream_t stream, int* counters = nullptr,
+                     const PeerOut* peer = nullptr);
 
 // Persistent stream-K GEMM: `ws` holds gemm_persistent_ws_floats() floats, `counters` >= num_sms zeroed ints
 // private to the stream (the kernel resets them).

@@ -154,7 +154,9 @@ class CausalLM(nn.Module):
         tp = self.tp
         if not partial or tp is None or tp.size == 1:
             return ops.rmsnorm(h, weight, eps, resid)
-        if tp.fused and tp.comm is not None and tp.comm.fits(h.numel() // h.shape[-1]):
+        from ..parallel.comm import Pushed
+
+        if isinstance(h, Pushed) or (tp.fused and tp.comm is not None and tp.comm.fits(h.numel() // h.shape[-1])):
             return tp.comm.reduce_rmsnorm(h, weight, eps, resid)
         return ops.rmsnorm(tp.all_reduce(h), weight, eps, resid)
 
@@ -168,14 +170,23 @@ class CausalLM(nn.Module):
                            v_cache, batch.kv_len, batch.n_new, layer.q_norm, layer.k_norm, c.rms_norm_eps,
                            q_offset=batch.q_offset)
         o = ops.attention(q, k_cache, v_cache, batch.kv_len, batch.n_new, batch.mask, q_offset=batch.q_offset)
-        return ops.linear(o.reshape(*o.shape[:2], -1), layer.wo)
+        return self._row_linear(o.reshape(*o.shape[:2], -1), layer.wo)
+
+    def _row_linear(self, x: torch.Tensor, weight: torch.Tensor):
+        """A row-parallel projection (``wo``, ``w_down``): under fused tensor parallelism the GEMM pushes its
+        partial output to the peers itself and returns a :class:`~economize_b200.parallel.comm.Pushed` marker."""
+        tp = self.tp
+        if tp is not None and tp.size > 1 and tp.fused and tp.comm is not None \
+                and tp.comm.fits(x.numel() // x.shape[-1]):
+            return tp.comm.gemm_push(x, weight)
+        return ops.linear(x, weight)
 
     def _mlp(self, layer: DecoderLayer, x: torch.Tensor) -> torch.Tensor:
         if layer.router is not None:
             from ..parallel.moe import moe_mlp
 
             return moe_mlp(x, layer.router, layer.w_gate_up, layer.w_down, self.config.experts_per_token)
-        return ops.linear(ops.silu_mul(ops.linear(x, layer.w_gate_up)), layer.w_down)
+        return self._row_linear(ops.silu_mul(ops.linear(x, layer.w_gate_up)), layer.w_down)
 
     def logits(self, hidden: torch.Tensor) -> torch.Tensor:
         """Logits over the full vocabulary (gathered from the vocabulary shards under tensor parallelism)."""

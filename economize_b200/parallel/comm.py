@@ -17,7 +17,14 @@ import torch.distributed as dist
 from .. import ops
 from ..errors import CommTimeoutError, ConfigError
 
-__all__ = ["FusedAllReduce"]
+__all__ = ["FusedAllReduce", "Pushed"]
+
+
+class Pushed:
+    """A row-parallel projection output that its GEMM already stored into every peer's slot (push mode)."""
+
+    def __init__(self, rows: int, shape: torch.Size, like: torch.Tensor, parity: int) -> None:
+        self.rows, self.shape, self.like, self.parity = rows, shape, like, parity
 
 
 class FusedAllReduce:
@@ -49,17 +56,32 @@ class FusedAllReduce:
     def fits(self, rows: int) -> bool:
         return rows <= self.max_tokens
 
-    def reduce_rmsnorm(self, partial: torch.Tensor, weight: torch.Tensor, eps: float,
-                       residual: torch.Tensor | None) -> tuple[torch.Tensor, torch.Tensor]:
-        """``(rmsnorm(sum_ranks(partial) + residual) * weight, sum_ranks(partial) + residual)``."""
-        shape = partial.shape
-        rows = partial.numel() // self.hidden
+    def gemm_push(self, x: torch.Tensor, weight: torch.Tensor) -> Pushed:
+        """Row-parallel ``x @ weight.T`` whose output tiles the GEMM stores straight into every peer's slot (the
+        GEMM -> all-reduce fusion); :meth:`reduce_rmsnorm` consumes the result."""
+        shape = (*x.shape[:-1], weight.shape[0])
+        rows = x.numel() // x.shape[-1]
         parity = self.calls % 2
         self.calls += 1
-        self.ext.push(partial.reshape(rows, self.hidden), self.ptrs, self.tp.rank, parity, self.slot_elems)
+        self.ext.linear_push(x.reshape(rows, x.shape[-1]), weight, self.ptrs, self.tp.rank, parity,
+                             self.slot_elems)
+        return Pushed(rows, torch.Size(shape), x, parity)
+
+    def reduce_rmsnorm(self, partial: torch.Tensor | Pushed, weight: torch.Tensor, eps: float,
+                       residual: torch.Tensor | None) -> tuple[torch.Tensor, torch.Tensor]:
+        """``(rmsnorm(sum_ranks(partial) + residual) * weight, sum_ranks(partial) + residual)``."""
+        if isinstance(partial, Pushed):
+            shape, rows, parity, like = partial.shape, partial.rows, partial.parity, partial.like
+        else:
+            shape = partial.shape
+            rows = partial.numel() // self.hidden
+            parity = self.calls % 2
+            self.calls += 1
+            like = partial
+            self.ext.push(partial.reshape(rows, self.hidden), self.ptrs, self.tp.rank, parity, self.slot_elems)
         res = None if residual is None else residual.reshape(rows, self.hidden)
         out, resid = self.ext.reduce_rmsnorm(self.ptrs, self.tp.rank, parity, self.slot_elems, res, weight,
-                                             float(eps), rows, self.hidden, partial)
+                                             float(eps), rows, self.hidden, like)
         return out.reshape(shape), resid.reshape(shape)
 
     def check(self) -> None:
