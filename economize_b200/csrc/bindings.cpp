@@ -231,13 +231,9 @@ Tensor linear(Tensor x, Tensor w) {
     rc = ecz::launch_gemm_persistent(tw, tx, y.data_ptr(), ws.data_ptr<float>(), split_counters(x.device(), stream),
                                      M, N, K, sms, status_word(x.device()), stream);
   } else {
-    // fewer tiles than SMs: split K evenly, reduced inside the kernel by each tile's last CTA
-    const int splits = ecz::gemm_splits(M, N, K, sms);
-    Tensor ws;
-    if (splits > 1) ws = at::empty({static_cast<int64_t>(splits) * M * N}, x.options().dtype(at::kFloat));
-    rc = ecz::launch_gemm_bf16(tw, tx, y.data_ptr(), splits > 1 ? ws.data_ptr<float>() : nullptr, M, N, K, splits,
-                               status_word(x.device()), stream,
-                               splits > 1 ? split_counters(x.device(), stream) : nullptr);
+    // fewer tiles than SMs: split K over a cluster per tile, partials reduced over DSMEM
+    rc = ecz::launch_gemm_cluster(tw, tx, y.data_ptr(), M, N, K, ecz::gemm_cluster_splits(M, N, K, sms),
+                                  status_word(x.device()), stream);
   }
   TORCH_CHECK(rc == 0, "linear: K must be a multiple of 8 and N of 4");
   return y;
@@ -399,9 +395,7 @@ void linear_push(Tensor x, Tensor w, std::vector<int64_t> ptrs, int64_t rank, in
   const int M = static_cast<int>(x.size(0)), K = static_cast<int>(x.size(1)), N = static_cast<int>(w.size(0));
   TORCH_CHECK(static_cast<long>(M) * N <= slot_elems, "linear_push: output larger than the slot");
   const int sms = num_sms(x.get_device());
-  const int splits = ecz::gemm_splits(M, N, K, sms);
-  Tensor ws;
-  if (splits > 1) ws = at::empty({static_cast<int64_t>(splits) * M * N}, x.options().dtype(at::kFloat));
+  const int splits = ecz::gemm_cluster_splits(M, N, K, sms);
   ecz::PeerOut peer{};
   peer.ptrs = peer_ptrs(ptrs);
   peer.world = static_cast<int>(ptrs.size());
@@ -412,10 +406,8 @@ void linear_push(Tensor x, Tensor w, std::vector<int64_t> ptrs, int64_t rank, in
   const CUtensorMap* tw = tensor_map(w.data_ptr(), N, K, K, 128);
   const CUtensorMap* tx = tensor_map(x.data_ptr(), M, K, K, ecz::gemm_block_n(M));
   cudaStream_t stream = at::cuda::getCurrentCUDAStream();
-  const int rc = ecz::launch_gemm_bf16(tw, tx, nullptr, splits > 1 ? ws.data_ptr<float>() : nullptr, M, N, K, splits,
-                                       status_word(x.device()), stream,
-                                       splits > 1 ? split_counters(x.device(), stream) : nullptr, &peer);
-  TORCH_CHECK(rc == 0, "linear_push: unsupported shape");
+  const int rc = ecz::launch_gemm_cluster(tw, tx, nullptr, M, N, K, splits, status_word(x.device()), stream, &peer);
+  TORCH_CHECK(rc == 0, "linear_push: unsupported shape or launch failure");
 }
 
 void push(Tensor src, std::vector<int64_t> ptrs, int64_t rank, int64_t parity, int64_t slot_elems) {
@@ -465,6 +457,9 @@ std::tuple<int64_t, int64_t, int64_t> attention_plan(int64_t B, int64_t T, int64
 }
 
 int64_t gemm_splits(int64_t M, int64_t N, int64_t K, int64_t sms) { return ecz::gemm_splits(M, N, K, sms); }
+int64_t gemm_cluster_splits(int64_t M, int64_t N, int64_t K, int64_t sms) {
+  return ecz::gemm_cluster_splits(M, N, K, sms);
+}
 
 }  // namespace
 
@@ -495,4 +490,5 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("status", &status, "read and clear the device status word of bounded waits");
   m.def("attention_plan", &attention_plan, "(m_tiles, splits, chunks_per_split) of an attention launch");
   m.def("gemm_splits", &gemm_splits, "split-K factor of a GEMM launch");
+  m.def("gemm_cluster_splits", &gemm_cluster_splits, "cluster size of the cluster split-K GEMM");
 }

@@ -24,14 +24,20 @@ constexpr int kBM = 128;  // W rows per tile (UMMA M)
 constexpr int kBK = 64;   // K elements per stage (one 128-byte swizzle row)
 constexpr int kABytes = kBM * kBK * 2;
 
-template <int BN>
+// kOcc CTAs share an SM: the stage ring is sized so that they fit its 228 KB of shared memory.
+template <int BN, int kOcc = 1>
 struct GemmCfg {
   static constexpr int kBBytes = BN * kBK * 2;
   static constexpr int kStageBytes = kABytes + kBBytes;
-  static constexpr int kStages = std::min(8, (200 * 1024) / kStageBytes);
+  static constexpr int kStages = std::min(8, ((kOcc == 1 ? 200 : 100) * 1024) / kStageBytes);
   static constexpr int kTmemCols = BN < 32 ? 32 : BN;
   static constexpr int kSmem = kStages * kStageBytes + 1024 /*align*/ + 256 /*barriers*/;
 };
+
+// Skinny tiles (BN <= 64) run two CTAs per SM in the split kernels, so one CTA's prologue and epilogue overlap
+// the other's weight stream.
+template <int BN>
+constexpr int split_occupancy() { return BN <= 64 ? 2 : 1; }
 
 // Push mode (tensor-parallel row-parallel projections): output tiles go straight into slot `rank` of every peer's
 // receive buffer (bf16 [rows, N], parity `parity`), and the last tile writer of the grid announces the arrival to
@@ -285,6 +291,216 @@ int run_gemm(const CUtensorMap& tm_w, const CUtensorMap& tm_x, void* y, float* w
                static_cast<const float*>(ws), static_cast<bf16*>(y), total, splits);
   }
   return 0;
+}
+
+// ---------------------------------------------------------------------------------------------------------------
+// Cluster split-K GEMM (the main path when the tiles cannot cover the SMs)
+// ---------------------------------------------------------------------------------------------------------------
+// The `splits` K-slices of one output tile form a thread-block cluster (1 x 1 x splits). Every CTA runs the
+// TMA/UMMA pipeline over its K-slice, parks its fp32 partial [BN rows][128 features] in its own shared memory (the
+// drained stage ring), and after a cluster barrier reduces rows r = rank, rank + splits, ... by reading all partials
+// over DSMEM in split order (deterministic, independent of scheduling). No global workspace is touched.
+__device__ __forceinline__ uint32_t cluster_ctarank() {
+  uint32_t r;
+  asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+  return r;
+}
+
+__device__ __forceinline__ void cluster_sync() {
+  asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+
+// 16-byte load from CTA `rank`'s shared memory at the address `local_addr` has in this CTA. Not volatile: the
+// partials are immutable between the two cluster barriers, so the compiler may batch these loads.
+__device__ __forceinline__ float4 ld_dsmem_v4(uint32_t local_addr, uint32_t rank) {
+  uint32_t remote;
+  asm("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(remote) : "r"(local_addr), "r"(rank));
+  float4 v;
+  asm("ld.shared::cluster.v4.f32 {%0, %1, %2, %3}, [%4];" : "=f"(v.x), "=f"(v.y), "=f"(v.z), "=f"(v.w) : "r"(remote));
+  return v;
+}
+
+template <int BN>
+__global__ void __launch_bounds__(128, split_occupancy<BN>())
+    gemm_cluster_kernel(const __grid_constant__ CUtensorMap tm_w, const __grid_constant__ CUtensorMap tm_x,
+                        bf16* __restrict__ y, int M, int N, int K, int kb_per_split, unsigned* status, PeerOut peer) {
+  using Cfg = GemmCfg<BN, split_occupancy<BN>()>;
+  constexpr int S = Cfg::kStages;
+  static_assert(BN * kBM * 4 <= S * Cfg::kStageBytes, "the partial tile must fit the stage ring");
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* a_tiles = smem;
+  uint8_t* b_tiles = smem + S * kABytes;
+  float* partial = reinterpret_cast<float*>(smem);  // reused after the pipeline drained: [BN][128] fp32
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + S * Cfg::kStageBytes);
+  uint64_t* empty = full + S;
+  uint64_t* accum = empty + S;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(accum + 1);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+  pdl_trigger();
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int n0 = blockIdx.x * kBM, m0 = blockIdx.y * BN;
+  const int splits = static_cast<int>(gridDim.z);
+  const uint32_t rank = splits > 1 ? cluster_ctarank() : 0u;
+  const int total_kb = (K + kBK - 1) / kBK;
+  const int kb0 = static_cast<int>(blockIdx.z) * kb_per_split;
+  const int nkb = max(0, min(kb_per_split, total_kb - kb0));
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < S; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1);
+    }
+    mbar_init(accum, 1);
+    *abort_flag = 0;
+    fence_mbar_init();
+    tma_prefetch_desc(&tm_w);
+    tma_prefetch_desc(&tm_x);
+  }
+  __syncwarp();
+  if (warp == 0) tmem_alloc(tmem_slot, Cfg::kTmemCols);
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+
+  if (nkb > 0 && warp == 0 && lane == 0) {
+    const int pre = nkb < S ? nkb : S;
+    for (int kb = 0; kb < pre; ++kb) {  // weights first: they do not depend on the previous kernel
+      mbar_arrive_expect_tx(&full[kb], Cfg::kStageBytes);
+      tma_load_2d(a_tiles + kb * kABytes, &tm_w, &full[kb], (kb0 + kb) * kBK, n0);
+    }
+    pdl_wait();
+    for (int kb = 0; kb < pre; ++kb) tma_load_2d(b_tiles + kb * Cfg::kBBytes, &tm_x, &full[kb], (kb0 + kb) * kBK, m0);
+    for (int kb = pre; kb < nkb; ++kb) {
+      const int s = kb % S;
+      const uint32_t use = kb / S;
+      if (!mbar_wait(&empty[s], (use & 1u) ^ 1u, status, kStatusWaitEmpty, abort_flag)) break;
+      mbar_arrive_expect_tx(&full[s], Cfg::kStageBytes);
+      const int kx = (kb0 + kb) * kBK;
+      tma_load_2d(a_tiles + s * kABytes, &tm_w, &full[s], kx, n0);
+      tma_load_2d(b_tiles + s * Cfg::kBBytes, &tm_x, &full[s], kx, m0);
+    }
+  } else if (nkb > 0 && warp == 1 && lane == 0) {
+    constexpr uint32_t idesc = idesc_bf16_f32(kBM, BN);
+    for (int kb = 0; kb < nkb; ++kb) {
+      const int s = kb % S;
+      if (!mbar_wait(&full[s], (kb / S) & 1u, status, kStatusWaitFull, abort_flag)) break;
+      tc_fence_after();
+      const uint32_t a_addr = smem_u32(a_tiles + s * kABytes);
+      const uint32_t b_addr = smem_u32(b_tiles + s * Cfg::kBBytes);
+#pragma unroll
+      for (int kk = 0; kk < kBK / 16; ++kk) {
+        umma_bf16(tmem, desc_kmajor_sw128(a_addr + kk * 32), desc_kmajor_sw128(b_addr + kk * 32), idesc,
+                  (kb | kk) != 0 ? 1u : 0u);
+      }
+      umma_commit(&empty[s]);
+    }
+    umma_commit(accum);
+  }
+  __syncwarp();
+  if (nkb > 0) mbar_wait(accum, 0, status, kStatusWaitAccum, abort_flag);
+  pdl_wait();
+  __syncthreads();
+  tc_fence_after();
+  const bool ok = nkb > 0 && !*abort_flag;
+  const uint32_t lane_base = tmem + (static_cast<uint32_t>(warp * 32) << 16);
+  const int feat = warp * 32 + lane;  // this thread's TMEM lane = output feature n0 + feat
+  if (splits == 1) {
+    if (ok) {
+#pragma unroll 1
+      for (int c = 0; c < BN; c += 16) {
+        float v[16];
+        tmem_ld16(lane_base + c, v);
+        const int n = n0 + feat;
+        if (n < N) {
+#pragma unroll
+          for (int j = 0; j < 16; ++j) {
+            const int m = m0 + c + j;
+            if (m >= M) continue;
+            const bf16 o = __float2bfloat16(v[j]);
+            if (peer.world == 0) y[static_cast<size_t>(m) * N + n] = o;
+            else for (int p = 0; p < peer.world; ++p) peer_slot(peer, p)[static_cast<size_t>(m) * N + n] = o;
+          }
+        }
+      }
+    }
+  } else {
+    // park the partial (zeros after a failure, so the reduction still runs on every CTA of the cluster)
+#pragma unroll 1
+    for (int c = 0; c < BN; c += 16) {
+      float v[16];
+      tmem_ld16(lane_base + c, v);
+#pragma unroll
+      for (int j = 0; j < 16; ++j) partial[(c + j) * kBM + feat] = ok ? v[j] : 0.f;
+    }
+    cluster_sync();  // every partial of the tile is in place
+    // this CTA reduces rows j = rank + splits * i; thread t sums features [4 (t % 32), + 4) of rows i = t / 32 + 4k
+    const int cg = threadIdx.x & 31, rp = threadIdx.x >> 5;
+    const int n = n0 + cg * 4;
+    const uint32_t base_addr = smem_u32(partial);
+    for (int i = rp;; i += 4) {
+      const int j = static_cast<int>(rank) + splits * i;
+      const int m = m0 + j;
+      if (j >= BN || m >= M) break;
+      const uint32_t addr = base_addr + (j * kBM + cg * 4) * 4;
+      float4 acc = ld_dsmem_v4(addr, 0);
+      for (int r = 1; r < splits; ++r) {
+        const float4 v = ld_dsmem_v4(addr, r);
+        acc.x += v.x; acc.y += v.y; acc.z += v.z; acc.w += v.w;
+      }
+      if (n < N && ok) {
+        __nv_bfloat162 lo = __floats2bfloat162_rn(acc.x, acc.y);
+        __nv_bfloat162 hi = __floats2bfloat162_rn(acc.z, acc.w);
+        uint2 packed;
+        packed.x = *reinterpret_cast<uint32_t*>(&lo);
+        packed.y = *reinterpret_cast<uint32_t*>(&hi);
+        if (peer.world == 0) {
+          *reinterpret_cast<uint2*>(y + static_cast<size_t>(m) * N + n) = packed;
+        } else {
+          for (int p = 0; p < peer.world; ++p)
+            *reinterpret_cast<uint2*>(peer_slot(peer, p) + static_cast<size_t>(m) * N + n) = packed;
+        }
+      }
+    }
+    cluster_sync();  // no CTA leaves while another still reads its shared memory
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 0) tmem_dealloc(tmem, Cfg::kTmemCols);
+  if (peer.world > 0 && ok) push_signal(peer, true, gridDim.x * gridDim.y * gridDim.z);
+}
+
+template <int BN>
+int run_gemm_cluster(const CUtensorMap& tm_w, const CUtensorMap& tm_x, void* y, int M, int N, int K, int splits,
+                     unsigned* status, cudaStream_t stream, const PeerOut& peer) {
+  using Cfg = GemmCfg<BN, split_occupancy<BN>()>;
+  static bool configured = false;
+  if (!configured) {
+    cudaFuncSetAttribute(gemm_cluster_kernel<BN>, cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg::kSmem);
+    configured = true;
+  }
+  const int total_kb = (K + kBK - 1) / kBK;
+  const int kbps = (total_kb + splits - 1) / splits;
+  splits = (total_kb + kbps - 1) / kbps;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3((N + kBM - 1) / kBM, (M + BN - 1) / BN, splits);
+  cfg.blockDim = dim3(128);
+  cfg.dynamicSmemBytes = Cfg::kSmem;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[2];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = pdl_enabled() ? 1 : 0;
+  attr[1].id = cudaLaunchAttributeClusterDimension;
+  attr[1].val.clusterDim.x = 1;
+  attr[1].val.clusterDim.y = 1;
+  attr[1].val.clusterDim.z = splits;
+  cfg.attrs = attr;
+  cfg.numAttrs = 2;
+  const cudaError_t err = cudaLaunchKernelEx(&cfg, gemm_cluster_kernel<BN>, tm_w, tm_x, static_cast<bf16*>(y), M, N,
+                                             K, kbps, status, peer);
+  return err == cudaSuccess ? 0 : -2;
 }
 
 // ---------------------------------------------------------------------------------------------------------------
@@ -544,6 +760,26 @@ int gemm_splits(int M, int N, int K, int num_sms) {
   int splits = num_sms / tiles;
   splits = std::min(splits, total_kb / 4);
   return std::max(1, std::min(splits, 16));
+}
+
+// Split count of the cluster split-K kernel: the gemm_splits rule over the CTA slots (two per SM for skinny
+// tiles), capped at 8 CTAs per (portable) cluster. Identical for every M up to 64 rows.
+int gemm_cluster_splits(int M, int N, int K, int num_sms) {
+  const int slots = gemm_block_n(M) <= 64 ? 2 * num_sms : num_sms;
+  return std::min(8, gemm_splits(M, N, K, slots));
+}
+
+int launch_gemm_cluster(const CUtensorMap* tm_w, const CUtensorMap* tm_x, void* y, int M, int N, int K, int splits,
+                        unsigned* status, cudaStream_t stream, const PeerOut* peer) {
+  if (K % 8 != 0 || N % 4 != 0 || splits < 1 || splits > 8) return -1;
+  const PeerOut none{};
+  const PeerOut& pe = peer != nullptr ? *peer : none;
+  switch (gemm_block_n(M)) {
+    case 32: return run_gemm_cluster<32>(*tm_w, *tm_x, y, M, N, K, splits, status, stream, pe);
+    case 64: return run_gemm_cluster<64>(*tm_w, *tm_x, y, M, N, K, splits, status, stream, pe);
+    case 128: return run_gemm_cluster<128>(*tm_w, *tm_x, y, M, N, K, splits, status, stream, pe);
+    default: return run_gemm_cluster<256>(*tm_w, *tm_x, y, M, N, K, splits, status, stream, pe);
+  }
 }
 
 int gemm_persistent_ctas(int M, int N, int K, int num_sms) {

@@ -55,6 +55,11 @@ int launch_gemm_bf16(const CUtensorMap* tm_w, const CUtensorMap* tm_x, void* y, 
                      int splits, unsigned* status, cudaStream_t stream, int* counters = nullptr,
                      const PeerOut* peer = nullptr);
 
+// Cluster split-K GEMM (partials reduced over DSMEM inside each tile's cluster; no workspace).
+int gemm_cluster_splits(int M, int N, int K, int num_sms);
+int launch_gemm_cluster(const CUtensorMap* tm_w, const CUtensorMap* tm_x, void* y, int M, int N, int K, int splits,
+                        unsigned* status, cudaStream_t stream, const PeerOut* peer = nullptr);
+
 // Persistent stream-K GEMM: `ws` holds gemm_persistent_ws_floats() floats, `counters` >= num_sms zeroed ints
 // private to the stream (the kernel resets them).
 int gemm_persistent_ctas(int M, int N, int K, int num_sms);
