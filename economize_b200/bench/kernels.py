@@ -1,0 +1,163 @@
+"""Kernel micro-benchmarks: ``python -m economize_b200.bench.kernels <op> [options]``.
+
+Each op times the engine's kernel (and, where one exists, the library baseline on the same shapes) with
+:func:`~economize_b200.bench.timing.time_call` (CUDA events per call, L2 flushed before every call, warm-up first)
+and prints one JSON line with the median time, the algorithmic bytes/FLOPs and the fraction of the measured
+peaks. Ops:
+
+* ``gemm``       bf16 ``x[M, K] @ w[N, K]^T`` (tcgen05 swap-AB GEMM vs cuBLAS through torch.matmul)
+* ``gemm_wq``    weight-only int4 / int8 / fp8 GEMM (``--fmt``), vs the bf16 kernel on the same shape
+* ``attention``  tree-masked decode attention over a bf16 slot cache (``--tree`` new tokens per row)
+* ``layer``      one Llama-3.1-8B decoder layer's projections as a CUDA graph (``--tp`` shard), ours vs cuBLAS
+
+``--once`` runs a single call without timing (the case a profiler captures).
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import sys
+
+import torch
+
+from .cost_model import HARDWARE
+from .timing import time_call
+
+__all__ = ["main"]
+
+
+def _peaks() -> tuple[float, float]:
+    hw = HARDWARE["b200"]
+    return hw.hbm_gbs, hw.bf16_tflops
+
+
+def _report(name: str, shape: dict, ms: float, nbytes: float, flops: float, baseline_ms: float | None = None):
+    hbm, tflops = _peaks()
+    out = {"op": name, **shape, "us": round(ms * 1e3, 2), "GB_s": round(nbytes / ms / 1e6, 1),
+           "TFLOP_s": round(flops / ms / 1e9, 1), "hbm_frac_of_measured": round(nbytes / ms / 1e6 / hbm, 3),
+           "tensor_frac_of_measured": round(flops / ms / 1e9 / tflops, 3)}
+    if baseline_ms is not None:
+        out["baseline_us"] = round(baseline_ms * 1e3, 2)
+        out["speedup"] = round(baseline_ms / ms, 3)
+    print(json.dumps(out))
+    sys.stdout.flush()
+
+
+def bench_gemm(a) -> None:
+    from .. import ops
+
+    dev = torch.device("cuda")
+    x = torch.randn(a.m, a.k, device=dev).bfloat16()
+    w = (torch.randn(a.n, a.k, device=dev) * 0.02).bfloat16()
+    if a.once:
+        ops.linear(x, w)
+        torch.cuda.synchronize()
+        return
+    ours = time_call(lambda: ops.linear(x, w), a.iters, a.warmup).median_ms
+    base = time_call(lambda: torch.matmul(x, w.t()), a.iters, a.warmup).median_ms
+    nbytes = 2 * (a.m * a.k + a.n * a.k + a.m * a.n)
+    _report("gemm", {"M": a.m, "N": a.n, "K": a.k}, ours, nbytes, 2 * a.m * a.n * a.k, base)
+
+
+def bench_gemm_wq(a) -> None:
+    from .. import ops
+    from ..techniques.quant import rtn
+
+    dev = torch.device("cuda")
+    x = torch.randn(a.m, a.k, device=dev).bfloat16()
+    w = torch.randn(a.n, a.k, device=dev) * 0.02
+    qw = rtn(w, a.fmt, a.group, a.fmt != "int4")
+    wb = w.bfloat16()
+    if a.once:
+        ops.linear(x, qw)
+        torch.cuda.synchronize()
+        return
+    ours = time_call(lambda: ops.linear(x, qw), a.iters, a.warmup).median_ms
+    bf16 = time_call(lambda: ops.linear(x, wb), a.iters, a.warmup).median_ms
+    nbytes = qw.nbytes() + 2 * (a.m * a.k + a.m * a.n)
+    _report(f"gemm_{a.fmt}", {"M": a.m, "N": a.n, "K": a.k, "group": a.group}, ours, nbytes, 2 * a.m * a.n * a.k,
+            bf16)
+
+
+def bench_attention(a) -> None:
+    from .. import ops
+    from ..decoding.tree import ancestor_bits
+
+    dev = torch.device("cuda")
+    B, T, H, Hkv, D = a.batch, a.tree, 32 // a.tp, 8 // a.tp, 128
+    S = ((a.ctx + T + 127) // 128) * 128
+    k = torch.randn(B, Hkv, S, D, device=dev).bfloat16()
+    v = torch.randn(B, Hkv, S, D, device=dev).bfloat16()
+    q = torch.randn(B, T, H, D, device=dev).bfloat16()
+    kv_len = torch.full((B,), a.ctx, dtype=torch.int32, device=dev)
+    n_new = torch.full((B,), T, dtype=torch.int32, device=dev)
+    parents = torch.arange(-1, T - 1, device=dev)[None].expand(B, T)  # a chain (worst case: full depth)
+    mask = ancestor_bits(parents.contiguous(), T) if T > 1 else None
+    if a.once:
+        ops.attention(q, k, v, kv_len, n_new, mask)
+        torch.cuda.synchronize()
+        return
+    ours = time_call(lambda: ops.attention(q, k, v, kv_len, n_new, mask), a.iters, a.warmup).median_ms
+    nbytes = 2 * (2 * B * Hkv * (a.ctx + T) * D + 2 * B * T * H * D)
+    flops = 4 * B * T * H * (a.ctx + T) * D
+    _report("attention", {"B": B, "T": T, "H": H, "Hkv": Hkv, "ctx": a.ctx}, ours, nbytes, flops)
+
+
+def bench_layer(a) -> None:
+    from .. import ops
+
+    dev = torch.device("cuda")
+    tp = a.tp
+    H, F, Q, KV = 4096, 14336 // tp, 4096 // tp, 1024 // tp
+    n_layers = 8
+
+    def mk(n, k):
+        return (torch.randn(n, k, device=dev) * 0.02).bfloat16()
+
+    layers = [dict(qkv=mk(Q + 2 * KV, H), o=mk(H, Q), gu=mk(2 * F, H), d=mk(H, F)) for _ in range(n_layers)]
+    x = torch.randn(a.m, H, device=dev).bfloat16()
+
+    def chain(lin):
+        h = x
+        for L in layers:
+            q = lin(h, L["qkv"])
+            o = lin(q[:, :Q].contiguous(), L["o"])
+            g = lin(o, L["gu"])
+            h = lin(g[:, :F].contiguous(), L["d"])
+        return h
+
+    res = {}
+    for name, lin in (("ours", ops.linear), ("cublas", lambda t, w: torch.matmul(t, w.t()))):
+        chain(lin)
+        torch.cuda.synchronize()
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g):
+            chain(lin)
+        res[name] = time_call(g.replay, a.iters, a.warmup, flush=False).median_ms / n_layers
+    nbytes = sum(v.numel() * 2 for v in layers[0].values())
+    flops = 2 * a.m * sum(v.numel() for v in layers[0].values())
+    _report("layer_projections", {"M": a.m, "tp": tp}, res["ours"], nbytes, flops, res["cublas"])
+
+
+def main(argv: list[str] | None = None) -> None:
+    p = argparse.ArgumentParser(description=__doc__.splitlines()[0])
+    p.add_argument("op", choices=["gemm", "gemm_wq", "attention", "layer"])
+    p.add_argument("--m", type=int, default=61)
+    p.add_argument("--n", type=int, default=6144)
+    p.add_argument("--k", type=int, default=4096)
+    p.add_argument("--fmt", default="int4", choices=["int4", "int8", "fp8"])
+    p.add_argument("--group", type=int, default=128)
+    p.add_argument("--batch", type=int, default=1)
+    p.add_argument("--tree", type=int, default=61)
+    p.add_argument("--ctx", type=int, default=768)
+    p.add_argument("--tp", type=int, default=1)
+    p.add_argument("--iters", type=int, default=20)
+    p.add_argument("--warmup", type=int, default=3)
+    p.add_argument("--once", action="store_true", help="one untimed call (for profiler captures)")
+    a = p.parse_args(argv)
+    {"gemm": bench_gemm, "gemm_wq": bench_gemm_wq, "attention": bench_attention, "layer": bench_layer}[a.op](a)
+
+
+if __name__ == "__main__":
+    main()

@@ -66,6 +66,8 @@ class EfficientModel(nn.Module):
         self._decoders: dict[tuple[DecodeConfig, str | None], SpecEngine] = {}
         self.decoding = decoding
         self.source_digests: dict[str, str] | None = None
+        #: fingerprint of the base weights taken before weight-rewriting techniques attached (else None)
+        self.teacher_digest: str | None = None
 
     def __getattr__(self, name: str) -> Any:
         try:
@@ -215,18 +217,31 @@ def build_model(model: nn.Module, configs: Sequence[TechniqueConfig], *, decodin
     techniques = [technique_for(c)(c, engine_model) for c in configs]
     techniques.sort(key=_rank)
     check_compatible(techniques)
+    digest = None
+    if any(Capability.WEIGHTS in t.capabilities for t in techniques):
+        from .serialization import teacher_fingerprint
+
+        digest = teacher_fingerprint(engine_model)
     for t in techniques:
         if states and t.name in states:
             t.load_technique_state(states[t.name])
         if hasattr(t, "calibrate") and calibration is not None:
             t.calibrate(calibration)
         t.attach()
+    for t in techniques:  # drafter-only weight transforms act once the drafter exists
+        if hasattr(t, "quantize_drafter"):
+            drafter = next((d for d in techniques if Capability.DRAFTER in d.capabilities), None)
+            if drafter is None:
+                raise ConfigError(f"{t.name} quantizes a drafter, but no drafting technique is applied")
+            t.quantize_drafter(drafter)
     if decoding is None:
         decoding = next((d for t in techniques if (d := t.default_decoding()) is not None), None)
     if decoding is None:
         decoding = DecodeConfig(cycle_length=4 if any(Capability.DRAFTER in t.capabilities for t in techniques)
                                 else 1)
-    return EfficientModel(engine_model, techniques, decoding, base_model=model)
+    result = EfficientModel(engine_model, techniques, decoding, base_model=model)
+    result.teacher_digest = digest
+    return result
 
 
 def apply(model: nn.Module, *configs: TechniqueConfig, decoding: DecodeConfig | None = None,

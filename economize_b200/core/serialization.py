@@ -128,7 +128,7 @@ def teacher_fingerprint(model: nn.Module, samples: int = 64) -> str:
     from ..models.llama import CausalLM
 
     if isinstance(model, CausalLM):
-        tensors = model.hf_state_dict()
+        tensors = model.hf_state_dict(copy=False)
     else:
         tensors = {k: v for k, v in model.state_dict().items()}
     h = hashlib.sha256()
@@ -154,7 +154,7 @@ def save(model: EfficientModel, path: str | Path, *, extra_meta: Mapping[str, An
         "economize_version": API_LEVEL,
         "economize_b200_version": __version__,
         "base_model": getattr(getattr(base, "config", None), "_name_or_path", None),
-        "teacher_fingerprint": teacher_fingerprint(model.model),
+        "teacher_fingerprint": model.teacher_digest or teacher_fingerprint(model.model),
         "techniques": [nested_dict(t.config) for t in model.techniques.values()],
         "decoding": model.decoding.to_dict(),
     }
@@ -188,7 +188,7 @@ def attach(model: nn.Module, checkpoint: Checkpoint, decoding: DecodeConfig | No
                          calibration=calibration, states=checkpoint.states)
     recorded = checkpoint.meta.get("teacher_fingerprint")
     if check_teacher and recorded and checkpoint.meta.get("economize_b200_version"):
-        if teacher_fingerprint(result.model) != recorded:
+        if (result.teacher_digest or teacher_fingerprint(result.model)) != recorded:
             warnings.warn("the base model's weights differ from those the checkpoint was saved with",
                           TeacherMismatchWarning, stacklevel=2)
     return result

@@ -59,28 +59,34 @@ int* split_counters(const at::Device& device, cudaStream_t stream) {
   return it->second.data_ptr<int>();
 }
 
-// LRU cache of tensor maps keyed by (base, rows, cols, stride, box_rows).
+// LRU cache of tensor maps keyed by (base, element size, shape, stride, box, swizzle).
 struct MapKey {
   uintptr_t base;
   uint64_t rows, cols, stride;
-  uint32_t box;
+  uint32_t box_cols, box_rows;
+  int elem, swizzle;
   bool operator==(const MapKey& o) const {
-    return base == o.base && rows == o.rows && cols == o.cols && stride == o.stride && box == o.box;
+    return base == o.base && rows == o.rows && cols == o.cols && stride == o.stride && box_cols == o.box_cols &&
+           box_rows == o.box_rows && elem == o.elem && swizzle == o.swizzle;
   }
 };
 struct MapKeyHash {
   size_t operator()(const MapKey& k) const {
-    return std::hash<uintptr_t>()(k.base) ^ (k.rows * 1315423911u) ^ (k.cols << 7) ^ (k.stride << 17) ^ k.box;
+    return std::hash<uintptr_t>()(k.base) ^ (k.rows * 1315423911u) ^ (k.cols << 7) ^ (k.stride << 17) ^
+           (static_cast<uint64_t>(k.box_rows) << 3) ^ (static_cast<uint64_t>(k.box_cols) << 40) ^ (k.elem << 29) ^
+           (static_cast<uint64_t>(k.swizzle) << 50);
   }
 };
 
-const CUtensorMap* tensor_map(const void* base, uint64_t rows, uint64_t cols, uint64_t stride, uint32_t box) {
+// Tensor map of a row-major [rows, cols] matrix of `elem`-byte elements (row stride in bytes).
+const CUtensorMap* tensor_map_ex(const void* base, int elem, uint64_t rows, uint64_t cols, uint64_t stride_bytes,
+                                 uint32_t box_cols, uint32_t box_rows, int swizzle) {
   static std::mutex mu;
   static std::list<std::pair<MapKey, CUtensorMap>> lru;
   static std::unordered_map<MapKey, std::list<std::pair<MapKey, CUtensorMap>>::iterator, MapKeyHash> index;
   constexpr size_t kCap = 4096;
   std::lock_guard<std::mutex> lock(mu);
-  MapKey key{reinterpret_cast<uintptr_t>(base), rows, cols, stride, box};
+  MapKey key{reinterpret_cast<uintptr_t>(base), rows, cols, stride_bytes, box_cols, box_rows, elem, swizzle};
   auto it = index.find(key);
   if (it != index.end()) {
     lru.splice(lru.begin(), lru, it->second);
@@ -88,7 +94,7 @@ const CUtensorMap* tensor_map(const void* base, uint64_t rows, uint64_t cols, ui
   }
   CUtensorMap map;
   std::memset(&map, 0, sizeof(map));
-  const int rc = ecz::make_tmap_2d_bf16(&map, base, rows, cols, stride, box);
+  const int rc = ecz::make_tmap_2d(&map, elem, base, rows, cols, stride_bytes, box_cols, box_rows, swizzle);
   TORCH_CHECK(rc == 0, "cuTensorMapEncodeTiled failed (code ", rc, ") for rows=", rows, " cols=", cols);
   lru.emplace_front(key, map);
   index[key] = lru.begin();
@@ -97,6 +103,12 @@ const CUtensorMap* tensor_map(const void* base, uint64_t rows, uint64_t cols, ui
     lru.pop_back();
   }
   return &lru.front().second;
+}
+
+// bf16 [rows, cols] (row stride in elements) with a {64, box} box and the 128-byte swizzle: the GEMM/attention
+// operand layout.
+const CUtensorMap* tensor_map(const void* base, uint64_t rows, uint64_t cols, uint64_t stride, uint32_t box) {
+  return tensor_map_ex(base, 2, rows, cols, stride * 2, 64, box, 128);
 }
 
 std::tuple<Tensor, Tensor> rmsnorm(Tensor x, Tensor w, double eps, c10::optional<Tensor> resid) {
@@ -236,6 +248,47 @@ Tensor linear(Tensor x, Tensor w) {
                                   status_word(x.device()), stream);
   }
   TORCH_CHECK(rc == 0, "linear: K must be a multiple of 8 and N of 4");
+  return y;
+}
+
+// Weight-only quantized linear: x [M, K] bf16, packed uint8 weights [N, K * bits / 8], scales (and int4 zeros)
+// bf16 [K / group, N]; fmt 0 int4, 1 int8, 2 fp8-e4m3.
+Tensor linear_wq(Tensor x, Tensor qweight, Tensor scales, c10::optional<Tensor> zeros, int64_t fmt, int64_t group,
+                 int64_t splits) {
+  CHECK_CUDA(x);
+  CHECK_BF16(x);
+  CHECK_BF16(scales);
+  TORCH_CHECK(qweight.scalar_type() == at::kByte, "qweight must be uint8");
+  TORCH_CHECK(fmt >= 0 && fmt <= 2, "unknown weight format ", fmt);
+  TORCH_CHECK(x.dim() == 2 && qweight.dim() == 2 && scales.dim() == 2, "linear_wq expects 2-D operands");
+  c10::cuda::CUDAGuard guard(x.device());
+  x = x.contiguous();
+  TORCH_CHECK(qweight.is_contiguous() && scales.is_contiguous(), "packed weights and scales must be contiguous");
+  const int M = static_cast<int>(x.size(0)), K = static_cast<int>(x.size(1)), N = static_cast<int>(qweight.size(0));
+  const int row_bytes = fmt == ecz::kWqInt4 ? K / 2 : K;
+  TORCH_CHECK(qweight.size(1) == row_bytes, "qweight has ", qweight.size(1), " bytes per row, expected ", row_bytes);
+  TORCH_CHECK(K % group == 0 && scales.size(0) == K / group && scales.size(1) == N, "scales must be [K / group, N]");
+  TORCH_CHECK(K % 64 == 0 && group % 64 == 0 && N % 8 == 0, "linear_wq: K and group must be multiples of 64, N of 8");
+  Tensor z;
+  if (fmt == ecz::kWqInt4) {
+    TORCH_CHECK(zeros.has_value(), "int4 weights need zeros");
+    z = zeros->contiguous();
+    CHECK_BF16(z);
+    TORCH_CHECK(z.sizes() == scales.sizes(), "zeros must match scales");
+  }
+  auto y = at::empty({M, N}, x.options());
+  if (M == 0) return y;
+  const int bn = ecz::gemm_block_n(M);
+  ecz::WqMaps maps;
+  maps.w = tensor_map_ex(qweight.data_ptr(), 1, N, row_bytes, row_bytes, fmt == ecz::kWqInt4 ? 32 : 64, 128, 0);
+  maps.s = tensor_map_ex(scales.data_ptr(), 2, K / group, N, static_cast<uint64_t>(N) * 2, 128, 1, 0);
+  if (fmt == ecz::kWqInt4) maps.z = tensor_map_ex(z.data_ptr(), 2, K / group, N, static_cast<uint64_t>(N) * 2, 128, 1, 0);
+  maps.x = tensor_map(x.data_ptr(), M, K, K, bn);
+  const int sp = splits > 0 ? static_cast<int>(splits)
+                            : ecz::gemm_wq_splits(M, N, K, static_cast<int>(fmt), num_sms(x.get_device()));
+  const int rc = ecz::launch_gemm_wq(maps, y.data_ptr(), M, N, K, static_cast<int>(group), static_cast<int>(fmt), sp,
+                                     status_word(x.device()), at::cuda::getCurrentCUDAStream());
+  TORCH_CHECK(rc == 0, "linear_wq: launch failed (", rc, ")");
   return y;
 }
 
@@ -472,6 +525,8 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
         py::arg("scale"), py::arg("q_offset"), py::arg("trace") = py::none());
   m.def("silu_mul", &silu_mul, "SwiGLU activation of [gate; up]");
   m.def("linear", &linear, "x @ w.T on tcgen05 (swap-AB, split-K)");
+  m.def("linear_wq", &linear_wq, "weight-only quantized x @ dequant(w).T (int4 / int8 / fp8 weights)", py::arg("x"),
+        py::arg("qweight"), py::arg("scales"), py::arg("zeros"), py::arg("fmt"), py::arg("group"), py::arg("splits") = 0);
   m.def("argmax", &argmax, "row argmax");
   m.def("greedy_accept", &greedy_accept, "longest accepted path of a verified draft tree", py::arg("tokens"),
         py::arg("parents"), py::arg("pred"), py::arg("ok") = py::none());

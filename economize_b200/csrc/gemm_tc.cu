@@ -300,25 +300,6 @@ int run_gemm(const CUtensorMap& tm_w, const CUtensorMap& tm_x, void* y, float* w
 // TMA/UMMA pipeline over its K-slice, parks its fp32 partial [BN rows][128 features] in its own shared memory (the
 // drained stage ring), and after a cluster barrier reduces rows r = rank, rank + splits, ... by reading all partials
 // over DSMEM in split order (deterministic, independent of scheduling). No global workspace is touched.
-__device__ __forceinline__ uint32_t cluster_ctarank() {
-  uint32_t r;
-  asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
-  return r;
-}
-
-__device__ __forceinline__ void cluster_sync() {
-  asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
-}
-
-// 16-byte load from CTA `rank`'s shared memory at the address `local_addr` has in this CTA. Not volatile: the
-// partials are immutable between the two cluster barriers, so the compiler may batch these loads.
-__device__ __forceinline__ float4 ld_dsmem_v4(uint32_t local_addr, uint32_t rank) {
-  uint32_t remote;
-  asm("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(remote) : "r"(local_addr), "r"(rank));
-  float4 v;
-  asm("ld.shared::cluster.v4.f32 {%0, %1, %2, %3}, [%4];" : "=f"(v.x), "=f"(v.y), "=f"(v.z), "=f"(v.w) : "r"(remote));
-  return v;
-}
 
 template <int BN>
 __global__ void __launch_bounds__(128, split_occupancy<BN>())

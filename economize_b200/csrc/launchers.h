@@ -91,6 +91,23 @@ int launch_reduce_rmsnorm(const PeerPtrs& peers, int rank, int world, int parity
                           const void* w, void* out, void* resid_out, int rows, int hidden, float eps,
                           unsigned* status, cudaStream_t stream);
 
+// gemm_wq.cu: weight-only quantized GEMM (W4A16 / W8A16 / fp8-weight); see the file comment for the layouts.
+enum WqFormat : int { kWqInt4 = 0, kWqInt8 = 1, kWqFp8 = 2 };
+struct WqMaps {
+  const CUtensorMap* w = nullptr;  // packed weights, uint8 [N, K * bits / 8], box {64 * bits / 8, 128}
+  const CUtensorMap* s = nullptr;  // scales bf16 [K / group, N], box {128, 1}
+  const CUtensorMap* z = nullptr;  // zeros bf16 [K / group, N], box {128, 1} (int4 only)
+  const CUtensorMap* x = nullptr;  // activations bf16 [M, K], box {64, BN} with the 128-byte swizzle
+};
+int gemm_wq_splits(int M, int N, int K, int fmt, int num_sms);
+int launch_gemm_wq(const WqMaps& maps, void* y, int M, int N, int K, int group, int fmt, int splits,
+                   unsigned* status, cudaStream_t stream);
+
+// tmap.cpp: a 2-D tensor map over a row-major [rows, cols] matrix of 1- or 2-byte elements (elem_bytes), with a
+// {box_cols, box_rows} box and the given swizzle (0, 32, 64 or 128 bytes). Returns 0 on success.
+int make_tmap_2d(CUtensorMap* map, int elem_bytes, const void* base, uint64_t rows, uint64_t cols,
+                 uint64_t row_stride_bytes, uint32_t box_cols, uint32_t box_rows, int swizzle_bytes);
+
 // tmap.cpp: a 2-D bf16 tensor map over a row-major [rows, cols] matrix with a {64, box_rows} box and the 128-byte
 // swizzle (cols * 2 bytes must be a multiple of 16). Returns 0 on success.
 int make_tmap_2d_bf16(CUtensorMap* map, const void* base, uint64_t rows, uint64_t cols, uint64_t row_stride_elems,

@@ -61,33 +61,40 @@ def load_hf_state(model, state: dict[str, torch.Tensor]) -> None:
 
 
 @torch.no_grad()
-def export_hf_state(model) -> dict[str, torch.Tensor]:
-    """The Hugging Face state dict of ``model`` (split projections, ``transformers`` 5 names)."""
+def export_hf_state(model, copy: bool = True) -> dict[str, torch.Tensor]:
+    """The Hugging Face state dict of ``model`` (split projections, ``transformers`` 5 names); quantized projections
+    are dequantized. ``copy=False`` returns views where possible."""
+    from ..ops.quant import QWeight
+
     c = model.config
-    out = {"model.embed_tokens.weight": model.embed.detach().clone(), "model.norm.weight": model.norm.detach().clone()}
+
+    def full(t):
+        return t.dequantize() if isinstance(t, QWeight) else t.detach()
+
+    out = {"model.embed_tokens.weight": model.embed.detach(), "model.norm.weight": model.norm.detach()}
     if model.lm_head is not None:
-        out["lm_head.weight"] = model.lm_head.detach().clone()
+        out["lm_head.weight"] = model.lm_head.detach()
     for i, layer in enumerate(model.layers):
         p = f"model.layers.{i}."
-        q, k, v = layer.wqkv.detach().split([c.q_size, c.kv_size, c.kv_size], 0)
+        q, k, v = full(layer.wqkv).split([c.q_size, c.kv_size, c.kv_size], 0)
         for n, w in zip("qkv", (q, k, v)):
-            out[p + f"self_attn.{n}_proj.weight"] = w.clone()
+            out[p + f"self_attn.{n}_proj.weight"] = w
         if layer.bqkv is not None:
             for n, w in zip("qkv", layer.bqkv.detach().split([c.q_size, c.kv_size, c.kv_size], 0)):
-                out[p + f"self_attn.{n}_proj.bias"] = w.clone()
-        out[p + "self_attn.o_proj.weight"] = layer.wo.detach().clone()
+                out[p + f"self_attn.{n}_proj.bias"] = w
+        out[p + "self_attn.o_proj.weight"] = full(layer.wo)
         if layer.q_norm is not None:
-            out[p + "self_attn.q_norm.weight"] = layer.q_norm.detach().clone()
-            out[p + "self_attn.k_norm.weight"] = layer.k_norm.detach().clone()
-        out[p + "input_layernorm.weight"] = layer.attn_norm.detach().clone()
-        out[p + "post_attention_layernorm.weight"] = layer.mlp_norm.detach().clone()
+            out[p + "self_attn.q_norm.weight"] = layer.q_norm.detach()
+            out[p + "self_attn.k_norm.weight"] = layer.k_norm.detach()
+        out[p + "input_layernorm.weight"] = layer.attn_norm.detach()
+        out[p + "post_attention_layernorm.weight"] = layer.mlp_norm.detach()
         if c.is_moe:
-            out[p + "mlp.gate.weight"] = layer.router.detach().clone()
-            out[p + "mlp.experts.gate_up_proj"] = layer.w_gate_up.detach().clone()
-            out[p + "mlp.experts.down_proj"] = layer.w_down.detach().clone()
+            out[p + "mlp.gate.weight"] = layer.router.detach()
+            out[p + "mlp.experts.gate_up_proj"] = full(layer.w_gate_up)
+            out[p + "mlp.experts.down_proj"] = full(layer.w_down)
         else:
-            g, u = layer.w_gate_up.detach().chunk(2, 0)
-            out[p + "mlp.gate_proj.weight"] = g.clone()
-            out[p + "mlp.up_proj.weight"] = u.clone()
-            out[p + "mlp.down_proj.weight"] = layer.w_down.detach().clone()
-    return out
+            g, u = full(layer.w_gate_up).chunk(2, 0)
+            out[p + "mlp.gate_proj.weight"] = g
+            out[p + "mlp.up_proj.weight"] = u
+            out[p + "mlp.down_proj.weight"] = full(layer.w_down)
+    return {k: v.clone() for k, v in out.items()} if copy else out

@@ -75,6 +75,8 @@ class CausalLM(nn.Module):
         self.lm_head = None if config.tie_word_embeddings else nn.Parameter(
             torch.empty(config.vocab_size, config.hidden_size, **kw))
         self._rope: tuple[torch.Tensor, torch.Tensor] | None = None
+        #: calibration hook ``observer(layer, name, x)`` called with the input of every projection (or None)
+        self.observer = None
         #: tensor-parallel group (set by economize_b200.parallel.tp.shard_model) and this rank's shard sizes
         self.tp = None
         self.local = dict(num_heads=config.num_heads, num_kv_heads=config.num_kv_heads,
@@ -137,7 +139,7 @@ class CausalLM(nn.Module):
                 aux[i] = resid
             h = self._attention(layer, i, x, batch, cache, cos, sin)
             x, resid = self._norm(h, layer.mlp_norm, resid, True)
-            h = self._mlp(layer, x)
+            h = self._mlp(layer, x, i)
             partial = True
         out, resid = self._norm(h, self.norm, resid, partial)
         if c.num_layers in capture:
@@ -163,6 +165,8 @@ class CausalLM(nn.Module):
     def _attention(self, layer: DecoderLayer, index: int, x: torch.Tensor, batch: StepBatch, cache: KVCache,
                    cos: torch.Tensor, sin: torch.Tensor) -> torch.Tensor:
         c = self.config
+        if self.observer is not None:
+            self.observer(index, "wqkv", x)
         qkv = ops.linear(x, layer.wqkv, layer.bqkv)
         k_cache, v_cache = cache.layer(index)
         q = ops.rope_store(qkv, batch.positions, cos, sin, self.local["num_heads"], self.local["num_kv_heads"],
@@ -170,23 +174,31 @@ class CausalLM(nn.Module):
                            v_cache, batch.kv_len, batch.n_new, layer.q_norm, layer.k_norm, c.rms_norm_eps,
                            q_offset=batch.q_offset)
         o = ops.attention(q, k_cache, v_cache, batch.kv_len, batch.n_new, batch.mask, q_offset=batch.q_offset)
-        return self._row_linear(o.reshape(*o.shape[:2], -1), layer.wo)
+        o = o.reshape(*o.shape[:2], -1)
+        if self.observer is not None:
+            self.observer(index, "wo", o)
+        return self._row_linear(o, layer.wo)
 
     def _row_linear(self, x: torch.Tensor, weight: torch.Tensor):
         """A row-parallel projection (``wo``, ``w_down``): under fused tensor parallelism the GEMM pushes its
         partial output to the peers itself and returns a :class:`~economize_b200.parallel.comm.Pushed` marker."""
         tp = self.tp
-        if tp is not None and tp.size > 1 and tp.fused and tp.comm is not None \
+        if tp is not None and tp.size > 1 and tp.fused and tp.comm is not None and isinstance(weight, torch.Tensor) \
                 and tp.comm.fits(x.numel() // x.shape[-1]):
             return tp.comm.gemm_push(x, weight)
         return ops.linear(x, weight)
 
-    def _mlp(self, layer: DecoderLayer, x: torch.Tensor) -> torch.Tensor:
+    def _mlp(self, layer: DecoderLayer, x: torch.Tensor, index: int = -1) -> torch.Tensor:
         if layer.router is not None:
             from ..parallel.moe import moe_mlp
 
             return moe_mlp(x, layer.router, layer.w_gate_up, layer.w_down, self.config.experts_per_token)
-        return self._row_linear(ops.silu_mul(ops.linear(x, layer.w_gate_up)), layer.w_down)
+        if self.observer is not None:
+            self.observer(index, "w_gate_up", x)
+        a = ops.silu_mul(ops.linear(x, layer.w_gate_up))
+        if self.observer is not None:
+            self.observer(index, "w_down", a)
+        return self._row_linear(a, layer.w_down)
 
     def logits(self, hidden: torch.Tensor) -> torch.Tensor:
         """Logits over the full vocabulary (gathered from the vocabulary shards under tensor parallelism)."""
@@ -219,10 +231,10 @@ class CausalLM(nn.Module):
         load_hf_state(model, hf_model.state_dict())
         return model
 
-    def hf_state_dict(self) -> dict[str, torch.Tensor]:
+    def hf_state_dict(self, copy: bool = True) -> dict[str, torch.Tensor]:
         from .hf import export_hf_state
 
-        return export_hf_state(self)
+        return export_hf_state(self, copy)
 
 
 @torch.no_grad()

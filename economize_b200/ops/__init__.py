@@ -11,6 +11,7 @@ import torch
 
 from . import reference
 from ._ext import available, load_error, require
+from .quant import QWeight
 
 __all__ = [
     "argmax",
@@ -23,6 +24,7 @@ __all__ = [
     "require",
     "rmsnorm",
     "ngram",
+    "QWeight",
     "rejection",
     "rope_store",
     "sample",
@@ -67,8 +69,12 @@ def silu_mul(gate_up: torch.Tensor) -> torch.Tensor:
     return reference.silu_mul(gate_up)
 
 
-def linear(x: torch.Tensor, weight: torch.Tensor, bias: torch.Tensor | None = None) -> torch.Tensor:
-    """``x @ weight.T (+ bias)``; on CUDA the tcgen05/TMA GEMM of ``csrc/gemm_tc.cu``."""
+def linear(x: torch.Tensor, weight, bias: torch.Tensor | None = None) -> torch.Tensor:
+    """``x @ weight.T (+ bias)``; on CUDA the tcgen05/TMA GEMM of ``csrc/gemm_tc.cu``, or for a quantized
+    :class:`~economize_b200.ops.quant.QWeight` the weight-only GEMM of ``csrc/gemm_wq.cu``."""
+    if isinstance(weight, QWeight):
+        y = weight.linear(x)
+        return y if bias is None else y + bias
     if x.is_cuda:
         shape = x.shape
         y = require().linear(x.reshape(-1, shape[-1]), weight)

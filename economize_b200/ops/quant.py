@@ -1,0 +1,177 @@
+"""Packed weight formats of the weight-only quantized GEMM (``csrc/gemm_wq.cu``) and their PyTorch reference.
+
+A :class:`QWeight` replaces a ``[N, K]`` bf16 weight of the engine model: ``ops.linear(x, qweight)`` runs the
+W4A16 / W8A16 tcgen05 kernel on CUDA tensors and ``x @ dequantize().T`` on the CPU. The quantization *methods*
+(round to nearest, GPTQ, AWQ) live in :mod:`economize_b200.techniques.quant`; this module only stores and unpacks.
+
+Formats (economize's ``QUANT_FORMATS`` names, ``src/economize/techniques/quant/grid.py:237-238``):
+
+* ``int4``: unsigned codes 0..15 with one zero point ``z`` and scale ``s`` per (output row, group):
+  ``w = (q - z) * s``. Packed two per byte with the nibble order ``k0 k2 k4 k6 k1 k3 k5 k7`` inside each 32-bit word
+  so the kernel extracts the bf16 pair ``(k_2i, k_2i+1)`` with one shift and one mask; zero points are stored as the
+  bf16 value ``128 + z``.
+* ``int8``: symmetric codes -128..127, ``w = q * s``; stored as ``q + 128`` with the byte order ``k0 k2 k1 k3`` per
+  word (the kernel splits each byte into nibbles to build exact bf16 values).
+* ``fp8``: e4m3 codes, ``w = q * s``.
+
+Scales (and zeros) are ``[K / group, N]`` bf16: one 256-byte row per 128 output features and group, which the kernel
+reads with one TMA box. The dequantized weight is ``bf16((q - z) * s)`` in every path (the kernel's bf16x2
+arithmetic rounds once, like the reference's fp32 product rounded to bf16).
+"""
+
+from __future__ import annotations
+
+import torch
+from torch import nn
+
+from ..errors import ConfigError
+
+__all__ = ["FORMAT_CODES", "QWeight", "dequantize", "install", "pack", "unpack"]
+
+#: kernel format codes (``WqFormat`` in ``csrc/launchers.h``)
+FORMAT_CODES = {"int4": 0, "int8": 1, "fp8": 2}
+_INT4_ORDER = (0, 2, 4, 6, 1, 3, 5, 7)
+_INT8_ORDER = (0, 2, 1, 3)
+
+
+def _words_to_bytes(words: torch.Tensor) -> torch.Tensor:
+    """int64 words holding 32-bit values ``[N, W]`` -> little-endian bytes ``[N, 4 W]`` uint8."""
+    shifts = torch.tensor([0, 8, 16, 24], device=words.device, dtype=torch.int64)
+    return ((words[..., None] >> shifts) & 0xFF).to(torch.uint8).reshape(words.shape[0], -1)
+
+
+def _bytes_to_words(data: torch.Tensor) -> torch.Tensor:
+    b = data.reshape(data.shape[0], -1, 4).to(torch.int64)
+    return b[..., 0] | (b[..., 1] << 8) | (b[..., 2] << 16) | (b[..., 3] << 24)
+
+
+def pack(codes: torch.Tensor, fmt: str) -> torch.Tensor:
+    """Pack integer codes ``[N, K]`` (int4: 0..15, int8: -128..127) or e4m3 values (fp8) into the kernel layout."""
+    n, k = codes.shape
+    if fmt == "int4":
+        c = codes.to(torch.int64).reshape(n, k // 8, 8)[..., list(_INT4_ORDER)]
+        words = torch.zeros(n, k // 8, dtype=torch.int64, device=codes.device)
+        for i in range(8):
+            words |= (c[..., i] & 0xF) << (4 * i)
+        return _words_to_bytes(words)
+    if fmt == "int8":
+        u = (codes.to(torch.int64) + 128).reshape(n, k // 4, 4)[..., list(_INT8_ORDER)]
+        return u.to(torch.uint8).reshape(n, k)
+    if fmt == "fp8":
+        return codes.to(torch.float8_e4m3fn).contiguous().view(torch.uint8)
+    raise ConfigError(f"unknown weight format {fmt!r}")
+
+
+def unpack(data: torch.Tensor, fmt: str) -> torch.Tensor:
+    """Inverse of :func:`pack`: int64 codes (int4, int8) or fp32 values (fp8) ``[N, K]``."""
+    n = data.shape[0]
+    if fmt == "int4":
+        words = _bytes_to_words(data)
+        nib = torch.stack([(words >> (4 * i)) & 0xF for i in range(8)], -1)  # in packed order
+        out = torch.empty_like(nib)
+        out[..., list(_INT4_ORDER)] = nib
+        return out.reshape(n, -1)
+    if fmt == "int8":
+        u = data.to(torch.int64).reshape(n, -1, 4)
+        out = torch.empty_like(u)
+        out[..., list(_INT8_ORDER)] = u
+        return out.reshape(n, -1) - 128
+    if fmt == "fp8":
+        return data.contiguous().view(torch.float8_e4m3fn).float()
+    raise ConfigError(f"unknown weight format {fmt!r}")
+
+
+def dequantize(qweight: torch.Tensor, scales: torch.Tensor, zeros: torch.Tensor | None, fmt: str, group: int,
+               dtype: torch.dtype = torch.bfloat16) -> torch.Tensor:
+    """``bf16((q - z) * s)`` as ``[N, K]`` in ``dtype`` (the value every kernel path multiplies with)."""
+    q = unpack(qweight, fmt).float()
+    s = scales.float().t().repeat_interleave(group, dim=1)  # [N, K]
+    if zeros is not None:
+        q = q - (zeros.float().t().repeat_interleave(group, dim=1) - 128.0)
+    return (q * s).to(torch.bfloat16).to(dtype)
+
+
+class QWeight(nn.Module):
+    """A quantized ``[out_features, in_features]`` weight (packed codes + scales (+ zeros) as buffers).
+
+    Args:
+        qweight: Packed codes (:func:`pack`).
+        scales: ``[K / group, N]`` bf16.
+        zeros: ``[K / group, N]`` bf16 holding ``128 + z`` (int4), else ``None``.
+        fmt: ``"int4"``, ``"int8"`` or ``"fp8"``.
+        group: Input columns per scale (``in_features`` for one scale per output row).
+        dtype: The activation dtype the layer computes in.
+    """
+
+    def __init__(self, qweight: torch.Tensor, scales: torch.Tensor, zeros: torch.Tensor | None, fmt: str, group: int,
+                 dtype: torch.dtype = torch.bfloat16) -> None:
+        super().__init__()
+        if fmt not in FORMAT_CODES:
+            raise ConfigError(f"unknown weight format {fmt!r}")
+        self.fmt = fmt
+        self.group = int(group)
+        self.out_features = int(qweight.shape[0])
+        self.in_features = int(qweight.shape[1] * (2 if fmt == "int4" else 1))
+        self.compute_dtype = dtype
+        self.register_buffer("qweight", qweight.contiguous())
+        self.register_buffer("scales", scales.to(torch.bfloat16).contiguous())
+        self.register_buffer("zeros", None if zeros is None else zeros.to(torch.bfloat16).contiguous())
+
+    @property
+    def shape(self) -> torch.Size:
+        return torch.Size((self.out_features, self.in_features))
+
+    @property
+    def device(self) -> torch.device:
+        return self.qweight.device
+
+    @property
+    def dtype(self) -> torch.dtype:
+        return self.compute_dtype
+
+    @property
+    def bits(self) -> int:
+        return 4 if self.fmt == "int4" else 8
+
+    def dequantize(self, dtype: torch.dtype | None = None) -> torch.Tensor:
+        return dequantize(self.qweight, self.scales, self.zeros, self.fmt, self.group, dtype or self.compute_dtype)
+
+    def nbytes(self) -> int:
+        return sum(t.numel() * t.element_size() for t in (self.qweight, self.scales, self.zeros) if t is not None)
+
+    def linear(self, x: torch.Tensor, splits: int = 0) -> torch.Tensor:
+        """``x @ dequantize().T`` (the tcgen05 kernel for CUDA bf16 inputs)."""
+        if x.is_cuda:
+            from ._ext import require
+
+            shape = x.shape
+            y = require().linear_wq(x.reshape(-1, shape[-1]).to(torch.bfloat16), self.qweight, self.scales,
+                                    self.zeros, FORMAT_CODES[self.fmt], self.group, int(splits))
+            return y.reshape(*shape[:-1], self.out_features).to(x.dtype)
+        w = self.dequantize(torch.float32)
+        return (x.float() @ w.t()).to(x.dtype)
+
+    def rows(self, start: int, stop: int) -> QWeight:
+        """The output rows ``[start, stop)`` (a column-parallel shard)."""
+        z = None if self.zeros is None else self.zeros[:, start:stop]
+        return QWeight(self.qweight[start:stop], self.scales[:, start:stop], z, self.fmt, self.group,
+                       self.compute_dtype)
+
+    def cols(self, start: int, stop: int) -> QWeight:
+        """The input columns ``[start, stop)`` (a row-parallel shard); both ends must sit on group boundaries."""
+        if start % self.group or stop % self.group:
+            raise ConfigError(f"column shard [{start}, {stop}) cuts a quantization group of {self.group}")
+        per = 2 if self.fmt == "int4" else 1
+        z = None if self.zeros is None else self.zeros[start // self.group: stop // self.group]
+        return QWeight(self.qweight[:, start // per: stop // per], self.scales[start // self.group: stop // self.group],
+                       z, self.fmt, self.group, self.compute_dtype)
+
+    def extra_repr(self) -> str:
+        return f"{self.out_features}x{self.in_features}, fmt={self.fmt}, group={self.group}"
+
+
+def install(owner: nn.Module, name: str, value) -> None:
+    """Put ``value`` (a :class:`QWeight` or a parameter) at ``owner.name``, replacing a parameter of that name."""
+    if name in owner._parameters and not isinstance(value, nn.Parameter):
+        del owner._parameters[name]
+    setattr(owner, name, value)

@@ -1,0 +1,171 @@
+"""Weight quantization: packed layouts, RTN / GPTQ / AWQ, the quant and draft_quant techniques, and the tcgen05
+weight-only GEMM against the fp32 product with the dequantized weights."""
+
+import pytest
+import torch
+
+import economize_b200 as eco
+from economize_b200 import ops
+from economize_b200.ops.quant import QWeight, dequantize, pack, unpack
+from economize_b200.techniques.eagle3 import Eagle3Config
+from economize_b200.techniques.quant import DraftQuantConfig, QuantConfig, gptq, rtn
+from economize_b200.techniques.quant.methods import collect
+
+from .helpers import prompts, reference_greedy, tiny_model
+
+
+@pytest.mark.parametrize("fmt", ["int4", "int8", "fp8"])
+def test_pack_roundtrip(fmt):
+    g = torch.Generator().manual_seed(0)
+    if fmt == "int4":
+        codes = torch.randint(0, 16, (24, 128), generator=g)
+    elif fmt == "int8":
+        codes = torch.randint(-128, 128, (24, 128), generator=g)
+    else:
+        codes = (torch.randn(24, 128, generator=g) * 50).to(torch.float8_e4m3fn).float()
+    packed = pack(codes, fmt)
+    assert packed.dtype == torch.uint8 and packed.shape == (24, 64 if fmt == "int4" else 128)
+    assert torch.equal(unpack(packed, fmt).to(codes.dtype), codes)
+
+
+def test_int4_nibble_order():
+    codes = torch.arange(8).repeat(2, 1)  # k0..k7 = 0..7
+    word = int.from_bytes(bytes(pack(codes, "int4")[0, :4].tolist()), "little")
+    assert [(word >> (4 * i)) & 0xF for i in range(8)] == [0, 2, 4, 6, 1, 3, 5, 7]
+
+
+@pytest.mark.parametrize("fmt,sym,tol", [("int4", False, 0.12), ("int4", True, 0.13), ("int8", True, 0.009),
+                                         ("fp8", True, 0.04)])
+def test_rtn_error(fmt, sym, tol):
+    w = torch.randn(64, 256) * 0.02
+    qw = rtn(w, fmt, 128, sym)
+    err = (qw.dequantize(torch.float32) - w).norm() / w.norm()
+    assert err < tol, err
+
+
+def test_gptq_beats_rtn_on_correlated_inputs():
+    g = torch.Generator().manual_seed(1)
+    mix = torch.randn(256, 256, generator=g) / 16
+    x = torch.randn(2048, 256, generator=g) @ mix  # correlated input channels
+    w = torch.randn(96, 256, generator=g) * 0.02
+    h = x.t() @ x
+    ref = x @ w.t()
+    e_rtn = (x @ rtn(w, "int4", 128, False).dequantize(torch.float32).t() - ref).norm()
+    e_gptq = (x @ gptq(w, h, "int4", 128, False).dequantize(torch.float32).t() - ref).norm()
+    e_order = (x @ gptq(w, h, "int4", 128, False, act_order=True).dequantize(torch.float32).t() - ref).norm()
+    assert e_gptq < 0.8 * e_rtn and e_order < 0.9 * e_rtn
+
+
+def test_qweight_shards():
+    w = torch.randn(32, 256) * 0.02
+    qw = rtn(w, "int4", 64, False)
+    full = qw.dequantize(torch.float32)
+    assert torch.equal(qw.rows(8, 24).dequantize(torch.float32), full[8:24])
+    assert torch.equal(qw.cols(64, 192).dequantize(torch.float32), full[:, 64:192])
+    with pytest.raises(eco.ConfigError):
+        qw.cols(32, 96)
+
+
+def test_collect_observes_every_projection():
+    model = tiny_model()
+    stats = collect(model, [torch.randint(0, 1024, (2, 9))], {0: ["wqkv", "wo", "w_gate_up", "w_down"]}, True, 8)
+    assert stats[(0, "wqkv")].n == 18 and stats[(0, "w_down")].sample.shape == (8, 688)
+    assert stats[(0, "wo")].hessian.shape == (256, 256)
+
+
+@pytest.mark.parametrize("method", ["rtn", "gptq", "awq"])
+def test_quant_technique_decodes(method):
+    model = tiny_model()
+    base = tiny_model()
+    cal = torch.randint(0, 1024, (2, 32), generator=torch.Generator().manual_seed(3))
+    eff = eco.apply(model, QuantConfig(format="int8", symmetric=True, method=method, group_size=128,
+                                       calibration_tokens=32), calibration=cal)
+    assert isinstance(eff.model.layers[0].wqkv, QWeight)
+    p = prompts((17,))[0]
+    h_q = eff(p[None])
+    h_f = eco.EfficientModel(base, [], eco.DecodeConfig())(p[None])
+    assert (h_q - h_f).norm() / h_f.norm() < 0.05  # int8 barely changes the logits
+    out = eff.decode(p, 8).tokens
+    assert torch.equal(out, reference_greedy(eff.model, p, 8))  # decoding stays exact for the quantized model
+
+
+def test_awq_fold_is_exact_before_rounding():
+    model = tiny_model()
+    ref_logits = eco.EfficientModel(tiny_model(), [], eco.DecodeConfig())(prompts((9,))[0][None])
+    cfg = QuantConfig(format="int4", method="awq", backend="fake", awq_clip=False, calibration_tokens=16)
+    eff = eco.apply(model, cfg, calibration=torch.randint(0, 1024, (1, 16)))
+    rel = (eff(prompts((9,))[0][None]) - ref_logits).norm() / ref_logits.norm()
+    assert rel < 0.5  # int4 of a random 256-wide model: close but not equal
+    assert any(k.endswith("attn_norm") for k in eff.techniques["quant"].replaced)
+
+
+def test_quant_save_load(tmp_path):
+    model = tiny_model()
+    eff = eco.apply(model, QuantConfig(format="int4", method="rtn"))
+    p = prompts((12,))[0]
+    before = eff(p[None])
+    eff.save_pretrained(str(tmp_path))
+    loaded = eco.load(tiny_model(), str(tmp_path))
+    assert isinstance(loaded.model.layers[2].wo, QWeight)
+    torch.testing.assert_close(loaded(p[None]), before)
+
+
+def test_draft_quant_keeps_decoding_lossless():
+    model = tiny_model()
+    eff = eco.apply(model, Eagle3Config(), DraftQuantConfig(format="int8"),
+                    decoding=eco.DecodeConfig(cycle_length=4))
+    tech = eff.techniques["eagle3"]
+    assert isinstance(tech.fc, QWeight) and isinstance(tech.layer.wo, QWeight)
+    p = prompts((20,))[0]
+    assert torch.equal(eff.decode(p, 12).tokens, reference_greedy(model, p, 12))
+
+
+def test_config_checks():
+    with pytest.raises(eco.ConfigError):
+        QuantConfig(format="int8", symmetric=False)
+    with pytest.raises(eco.ConfigError):
+        QuantConfig(group_size=100)
+    with pytest.raises(eco.ConfigError):
+        QuantConfig(method="gptq", format="fp8", symmetric=True)
+    with pytest.raises(eco.ConfigError):
+        eco.apply(tiny_model(), QuantConfig(method="gptq"))  # no calibration tokens
+
+
+# ---- GPU ------------------------------------------------------------------------------------------------------
+@pytest.mark.gpu
+@pytest.mark.parametrize("fmt", ["int4", "int8", "fp8"])
+@pytest.mark.parametrize("M,N,K,group", [(1, 4096, 4096, 128), (61, 6144, 4096, 128), (7, 264, 512, 64),
+                                         (200, 1024, 2048, 2048), (600, 512, 1024, 128)])
+def test_linear_wq_matches_fp32(cuda, fmt, M, N, K, group):
+    g = torch.Generator(device=cuda).manual_seed(0)
+    w = torch.randn(N, K, device=cuda, generator=g) * 0.02
+    qw = rtn(w, fmt, group, fmt != "int4")
+    x = torch.randn(M, K, device=cuda, generator=g).bfloat16()
+    y = ops.linear(x, qw)
+    exact = x.float() @ qw.dequantize(torch.float32).t()
+    torch.testing.assert_close(y.float(), exact, atol=2e-2, rtol=2e-2)
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("splits", [1, 2, 3, 8])
+def test_linear_wq_splits(cuda, splits):
+    g = torch.Generator(device=cuda).manual_seed(1)
+    qw = rtn(torch.randn(384, 2048, device=cuda, generator=g) * 0.02, "int4", 128, False)
+    x = torch.randn(40, 2048, device=cuda, generator=g).bfloat16()
+    y = qw.linear(x, splits=splits)
+    exact = x.float() @ qw.dequantize(torch.float32).t()
+    torch.testing.assert_close(y.float(), exact, atol=2e-2, rtol=2e-2)
+
+
+@pytest.mark.gpu
+def test_quantized_model_decodes_on_gpu(cuda):
+    from economize_b200.models.config import tiny_llama
+    from economize_b200.models.llama import CausalLM, init_weights
+
+    model = init_weights(CausalLM(tiny_llama(), torch.bfloat16, cuda), seed=0)
+    eff = eco.apply(model, QuantConfig(format="int4", method="rtn", group_size=128), Eagle3Config(),
+                    decoding=eco.DecodeConfig(cycle_length=4))
+    p = prompts((17,))[0].to(cuda)
+    plain = eff.decode(p, 16, decoding=eco.DecodeConfig(cycle_length=1)).tokens
+    spec = eff.decode(p, 16).tokens
+    assert torch.equal(spec.cpu(), plain.cpu())
