@@ -5,7 +5,9 @@ Each op times the engine's kernel (and, where one exists, the library baseline o
 and prints one JSON line with the median time, the algorithmic bytes/FLOPs and the fraction of the measured
 peaks. Ops:
 
-* ``gemm``       bf16 ``x[M, K] @ w[N, K]^T`` (tcgen05 swap-AB GEMM vs cuBLAS through torch.matmul)
+* ``gemm``       bf16 ``x[M, K] @ w[N, K]^T`` (tcgen05 swap-AB GEMM vs cuBLAS through torch.matmul); calls on
+  rotating weight copies (more than 2x L2 in total) are captured in one CUDA graph, so the per-call time excludes
+  launch overhead and reads the weights from HBM
 * ``gemm_wq``    weight-only int4 / int8 / fp8 GEMM (``--fmt``), vs the bf16 kernel on the same shape
 * ``attention``  tree-masked decode attention over a bf16 slot cache (``--tree`` new tokens per row)
 * ``layer``      one Llama-3.1-8B decoder layer's projections as a CUDA graph (``--tp`` shard), ours vs cuBLAS
@@ -22,7 +24,7 @@ import sys
 import torch
 
 from .cost_model import HARDWARE
-from .timing import time_call
+from .timing import L2_BYTES, time_call, time_graph
 
 __all__ = ["main"]
 
@@ -44,20 +46,26 @@ def _report(name: str, shape: dict, ms: float, nbytes: float, flops: float, base
     sys.stdout.flush()
 
 
+def _copies(nbytes: int) -> int:
+    """Distinct weight copies so that one pass over all of them streams at least 2x L2 from HBM."""
+    return max(2, -(-2 * L2_BYTES // max(nbytes, 1)))
+
+
 def bench_gemm(a) -> None:
     from .. import ops
 
     dev = torch.device("cuda")
     x = torch.randn(a.m, a.k, device=dev).bfloat16()
-    w = (torch.randn(a.n, a.k, device=dev) * 0.02).bfloat16()
+    n_copies = 1 if a.once else _copies(2 * a.n * a.k)
+    ws = [(torch.randn(a.n, a.k, device=dev) * 0.02).bfloat16() for _ in range(n_copies)]
     if a.once:
-        ops.linear(x, w)
+        ops.linear(x, ws[0])
         torch.cuda.synchronize()
         return
-    ours = time_call(lambda: ops.linear(x, w), a.iters, a.warmup).median_ms
-    base = time_call(lambda: torch.matmul(x, w.t()), a.iters, a.warmup).median_ms
+    ours = time_graph([lambda w=w: ops.linear(x, w) for w in ws], a.iters, a.warmup)
+    base = time_graph([lambda w=w: torch.matmul(x, w.t()) for w in ws], a.iters, a.warmup)
     nbytes = 2 * (a.m * a.k + a.n * a.k + a.m * a.n)
-    _report("gemm", {"M": a.m, "N": a.n, "K": a.k}, ours, nbytes, 2 * a.m * a.n * a.k, base)
+    _report("gemm", {"M": a.m, "N": a.n, "K": a.k, "copies": n_copies}, ours, nbytes, 2 * a.m * a.n * a.k, base)
 
 
 def bench_gemm_wq(a) -> None:
@@ -67,15 +75,16 @@ def bench_gemm_wq(a) -> None:
     dev = torch.device("cuda")
     x = torch.randn(a.m, a.k, device=dev).bfloat16()
     w = torch.randn(a.n, a.k, device=dev) * 0.02
-    qw = rtn(w, a.fmt, a.group, a.fmt != "int4")
-    wb = w.bfloat16()
+    qw0 = rtn(w, a.fmt, a.group, a.fmt != "int4")
     if a.once:
-        ops.linear(x, qw)
+        ops.linear(x, qw0)
         torch.cuda.synchronize()
         return
-    ours = time_call(lambda: ops.linear(x, qw), a.iters, a.warmup).median_ms
-    bf16 = time_call(lambda: ops.linear(x, wb), a.iters, a.warmup).median_ms
-    nbytes = qw.nbytes() + 2 * (a.m * a.k + a.m * a.n)
+    qws = [qw0] + [rtn(w, a.fmt, a.group, a.fmt != "int4") for _ in range(_copies(qw0.nbytes()) - 1)]
+    wbs = [w.bfloat16() for _ in range(_copies(2 * a.n * a.k))]
+    ours = time_graph([lambda q=q: ops.linear(x, q) for q in qws], a.iters, a.warmup)
+    bf16 = time_graph([lambda wb=wb: ops.linear(x, wb) for wb in wbs], a.iters, a.warmup)
+    nbytes = qw0.nbytes() + 2 * (a.m * a.k + a.m * a.n)
     _report(f"gemm_{a.fmt}", {"M": a.m, "N": a.n, "K": a.k, "group": a.group}, ours, nbytes, 2 * a.m * a.n * a.k,
             bf16)
 
@@ -98,7 +107,7 @@ def bench_attention(a) -> None:
         ops.attention(q, k, v, kv_len, n_new, mask)
         torch.cuda.synchronize()
         return
-    ours = time_call(lambda: ops.attention(q, k, v, kv_len, n_new, mask), a.iters, a.warmup).median_ms
+    ours = time_graph([lambda: ops.attention(q, k, v, kv_len, n_new, mask)] * 8, a.iters, a.warmup)
     nbytes = 2 * (2 * B * Hkv * (a.ctx + T) * D + 2 * B * T * H * D)
     flops = 4 * B * T * H * (a.ctx + T) * D
     _report("attention", {"B": B, "T": T, "H": H, "Hkv": Hkv, "ctx": a.ctx}, ours, nbytes, flops)
@@ -135,6 +144,7 @@ def bench_layer(a) -> None:
         with torch.cuda.graph(g):
             chain(lin)
         res[name] = time_call(g.replay, a.iters, a.warmup, flush=False).median_ms / n_layers
+        del g
     nbytes = sum(v.numel() * 2 for v in layers[0].values())
     flops = 2 * a.m * sum(v.numel() for v in layers[0].values())
     _report("layer_projections", {"M": a.m, "tp": tp}, res["ours"], nbytes, flops, res["cublas"])

@@ -15,7 +15,7 @@ from dataclasses import dataclass, field
 import torch
 import torch.distributed as dist
 
-__all__ = ["Timing", "max_over_ranks", "time_call"]
+__all__ = ["Timing", "max_over_ranks", "time_call", "time_graph"]
 
 L2_BYTES = 126 * 1024 * 1024
 
@@ -81,3 +81,30 @@ def time_call(fn: Callable[[], object], iters: int = 20, warmup: int = 3, flush:
     times = [s.elapsed_time(e) for s, e in zip(starts, ends)]
     return Timing([max_over_ranks(t, dev if dist.is_initialized() and dist.get_backend() == "nccl" else None)
                    for t in times])
+
+
+def time_graph(calls: list[Callable[[], object]], replays: int = 10, warmup: int = 3) -> float:
+    """Device milliseconds per call of ``calls`` captured back to back in one CUDA graph (launch overhead excluded).
+
+    Give the calls distinct inputs whose total size exceeds L2 (rotating weight copies) so that every call reads
+    from HBM, as it would inside a model step.
+    """
+    for fn in calls:
+        fn()
+    torch.cuda.synchronize()
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph):
+        for fn in calls:
+            fn()
+    for _ in range(warmup):
+        graph.replay()
+    torch.cuda.synchronize()
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    start.record()
+    for _ in range(replays):
+        graph.replay()
+    end.record()
+    torch.cuda.synchronize()
+    ms = start.elapsed_time(end) / (replays * len(calls))
+    del graph
+    return max_over_ranks(ms)

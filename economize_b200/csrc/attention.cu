@@ -15,7 +15,15 @@
 // Visibility of slot s for query token t of row b: s < kv_len[b] (committed prefix), or j = s - kv_len[b] < n_new[b]
 // and (bit j of mask[b, t], or j <= q_offset + t without a mask). The key range may be split over `splits` CTAs,
 // whose (O, max, sum) partials a merge kernel combines in log-sum-exp form (the split-K merge of the reference).
+//
+// fp8 caches (e4m3 codes with one static scale per KV head, K = s_k * K8, V = s_v * V8): TMA brings the raw
+// [128 keys, 128 B] code tiles into a double-buffered staging ring, all threads convert them to bf16 (exact: every
+// e4m3 value is a bf16 value) in the swizzled layout the UMMAs read, and the scales are applied outside the tensor
+// cores: s_k multiplies the softmax scale, s_v the output. This reads half the bytes of a bf16 cache (the
+// reference's fp8_kv decode path decodes the codes in registers, src/economize/attention/_decode_kernels.py:17).
 #include <algorithm>
+
+#include <cuda_fp8.h>
 
 #include "common.cuh"
 #include "launchers.h"
@@ -30,6 +38,9 @@ constexpr int kDim = 128;
 constexpr int kAtom = kRows * 128;          // bytes of one 64-column swizzled half tile (128 rows x 128 B)
 constexpr int kTile = 2 * kAtom;            // a 128 x 128 bf16 tile
 constexpr int kSmem = 6 * kTile + 1024 + 64 + 4 * 128 * 4;  // Q, P, 2 x K, 2 x V, barriers, row partials
+constexpr int kRawTile = kKeys * kDim;                        // one fp8 code tile (128 keys x 128 B)
+// fp8: Q, P, converted K, converted V, then 2 stages x (raw K, raw V): the same 6 x kTile
+static_assert(4 * kTile + 4 * kRawTile == 6 * kTile, "fp8 layout must fit the bf16 footprint");
 
 __device__ __forceinline__ void store_row_swizzled(uint8_t* tile, int r, int chunk, uint4 v) {
   // chunk in [0, 16): 16-byte chunk of a 256-byte row; chunks 0-7 in the first half tile, 8-15 in the second
@@ -37,6 +48,32 @@ __device__ __forceinline__ void store_row_swizzled(uint8_t* tile, int r, int chu
   const int c = chunk & 7;
   *reinterpret_cast<uint4*>(atom + r * 128 + ((c ^ (r & 7)) << 4)) = v;
 }
+
+// Convert one 128 x 128 e4m3 code tile (row-major, 128 B rows) into the bf16 swizzled two-atom tile; thread t of
+// 512 converts 32 codes of row t / 4.
+__device__ __forceinline__ void convert_fp8_tile(const uint8_t* raw, uint8_t* tile, int tid) {
+  const int row = tid >> 2, part = tid & 3;
+  const uint4* src = reinterpret_cast<const uint4*>(raw + row * kDim + part * 32);
+#pragma unroll
+  for (int h = 0; h < 2; ++h) {
+    const uint4 v = src[h];
+    const uint32_t w[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+    for (int u = 0; u < 2; ++u) {  // 8 codes -> one 16-byte chunk of 8 bf16
+      uint32_t o[4];
+#pragma unroll
+      for (int k = 0; k < 4; ++k) {
+        const uint32_t word = w[2 * u + k / 2];
+        const __nv_fp8x2_storage_t pair = static_cast<__nv_fp8x2_storage_t>((word >> (16 * (k & 1))) & 0xFFFFu);
+        const __half2 hv = __half2(__nv_cvt_fp8x2_to_halfraw2(pair, __NV_E4M3));
+        __nv_bfloat162 bv = __float22bfloat162_rn(__half22float2(hv));
+        o[k] = *reinterpret_cast<uint32_t*>(&bv);
+      }
+      store_row_swizzled(tile, row, part * 4 + h * 2 + u, make_uint4(o[0], o[1], o[2], o[3]));
+    }
+  }
+}
+
 
 // Visibility of the 32 slots [s0, s0 + 32) for one query row, bit i = slot s0 + i.
 __device__ __forceinline__ uint32_t visible32(int s0, int base, int nn, bool use_mask, uint64_t bits, int causal_lim,
@@ -70,18 +107,22 @@ __device__ __forceinline__ float fast_exp2(float x) {
 // [32 * (w / 4), 32 * (w / 4) + 32) of them (quarter q).
 constexpr int kThreads = 512;
 
+template <bool FP8>
 __global__ void __launch_bounds__(kThreads, 1)
     attn_tc_kernel(const bf16* __restrict__ q, const __grid_constant__ CUtensorMap tm_k,
                    const __grid_constant__ CUtensorMap tm_v, bf16* __restrict__ out, float* __restrict__ ws_o,
                    float* __restrict__ ws_ml, const int* __restrict__ kv_len, const int* __restrict__ n_new,
                    const int64_t* __restrict__ mask, int T, int H, int Hkv, int S, float scale_log2, int q_offset,
-                   int chunks_per_split, int m_tiles, unsigned* status, unsigned long long* trace) {
+                   int chunks_per_split, int m_tiles, unsigned* status, unsigned long long* trace,
+                   const float* __restrict__ k_scale, const float* __restrict__ v_scale) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* q_tile = smem;
   uint8_t* p_tile = smem + kTile;
+  // bf16: two stages of K and V tiles; fp8: one converted K and V tile, then two stages of raw codes
   uint8_t* k_tiles = smem + 2 * kTile;
-  uint8_t* v_tiles = smem + 4 * kTile;
+  uint8_t* v_tiles = FP8 ? smem + 3 * kTile : smem + 4 * kTile;
+  uint8_t* raw = smem + 4 * kTile;  // fp8 stage s: raw K at s * 2 * kRawTile, raw V after it
   uint64_t* kv_full = reinterpret_cast<uint64_t*>(smem + 6 * kTile);
   uint64_t* bar_s = kv_full + 2;
   uint64_t* bar_pv = bar_s + 1;
@@ -123,13 +164,20 @@ __global__ void __launch_bounds__(kThreads, 1)
 
   const size_t kv_row0 = (static_cast<size_t>(b) * Hkv + kvh) * S;
   auto issue_kv = [&](int c, int s) {
-    mbar_arrive_expect_tx(&kv_full[s], 4 * kAtom);
     const int y = static_cast<int>(kv_row0 + static_cast<size_t>(c) * kKeys);
-    tma_load_2d(k_tiles + s * kTile, &tm_k, &kv_full[s], 0, y);
-    tma_load_2d(k_tiles + s * kTile + kAtom, &tm_k, &kv_full[s], 64, y);
-    tma_load_2d(v_tiles + s * kTile, &tm_v, &kv_full[s], 0, y);
-    tma_load_2d(v_tiles + s * kTile + kAtom, &tm_v, &kv_full[s], 64, y);
+    if constexpr (FP8) {
+      mbar_arrive_expect_tx(&kv_full[s], 2 * kRawTile);
+      tma_load_2d(raw + s * 2 * kRawTile, &tm_k, &kv_full[s], 0, y);
+      tma_load_2d(raw + s * 2 * kRawTile + kRawTile, &tm_v, &kv_full[s], 0, y);
+    } else {
+      mbar_arrive_expect_tx(&kv_full[s], 4 * kAtom);
+      tma_load_2d(k_tiles + s * kTile, &tm_k, &kv_full[s], 0, y);
+      tma_load_2d(k_tiles + s * kTile + kAtom, &tm_k, &kv_full[s], 64, y);
+      tma_load_2d(v_tiles + s * kTile, &tm_v, &kv_full[s], 0, y);
+      tma_load_2d(v_tiles + s * kTile + kAtom, &tm_v, &kv_full[s], 64, y);
+    }
   };
+  if constexpr (FP8) scale_log2 *= k_scale[kvh];  // S = s_k * (Q . K8^T)
   if (tid == 0) {
     mbar_init(&kv_full[0], 1);
     mbar_init(&kv_full[1], 1);
@@ -180,9 +228,15 @@ __global__ void __launch_bounds__(kThreads, 1)
     ok = mbar_wait(&kv_full[s], kv_phase, status, kStatusWaitFull, abort_flag);
     if (!ok) break;
     if (stamp && i == 0) stamp[2] = global_timer_ns();
+    if constexpr (FP8) {  // the previous chunk's S MMA has completed: the converted K tile is free
+      convert_fp8_tile(raw + s * 2 * kRawTile, k_tiles, tid);
+      fence_async_smem();
+      tc_fence_before();
+      __syncthreads();
+    }
     if (tid == 0) {
       tc_fence_after();
-      const uint32_t qa = smem_u32(q_tile), ka = smem_u32(k_tiles + s * kTile);
+      const uint32_t qa = smem_u32(q_tile), ka = smem_u32(k_tiles + (FP8 ? 0 : s * kTile));
 #pragma unroll
       for (int kk = 0; kk < kDim / 16; ++kk) {
         const uint32_t off = (kk >> 2) * kAtom + (kk & 3) * 32;
@@ -191,6 +245,10 @@ __global__ void __launch_bounds__(kThreads, 1)
       umma_commit(bar_s);
     }
     __syncwarp();
+    if constexpr (FP8) {  // V converts while the S MMA runs (the previous PV MMA has completed)
+      convert_fp8_tile(raw + s * 2 * kRawTile + kRawTile, v_tiles, tid);
+      fence_async_smem();
+    }
     ok = mbar_wait(bar_s, ph, status, kStatusWaitAccum, abort_flag);
     if (!ok) break;
     __syncwarp();
@@ -234,9 +292,12 @@ __global__ void __launch_bounds__(kThreads, 1)
     fence_async_smem();
     tc_fence_before();
     __syncthreads();
+    if constexpr (FP8) {  // every thread has converted stage s: its raw codes may be overwritten
+      if (tid == 0 && c + 2 < c1) issue_kv(c + 2, s);
+    }
     if (tid == 0) {
       tc_fence_after();
-      const uint32_t pa = smem_u32(p_tile), va = smem_u32(v_tiles + s * kTile);
+      const uint32_t pa = smem_u32(p_tile), va = smem_u32(v_tiles + (FP8 ? 0 : s * kTile));
 #pragma unroll
       for (int kk = 0; kk < kKeys / 16; ++kk) {
         const uint32_t a_off = (kk >> 2) * kAtom + (kk & 3) * 32;
@@ -251,7 +312,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     __syncwarp();
     tc_fence_after();
     if (stamp && i == 0) stamp[5] = global_timer_ns();
-    if (tid == 0 && c + 2 < c1) issue_kv(c + 2, s);  // both MMAs reading stage s are done
+    if (!FP8 && tid == 0 && c + 2 < c1) issue_kv(c + 2, s);  // both MMAs reading stage s are done
     __syncwarp();
     float pv[32];
     tmem_ld16(tmem_pv + lane_off, pv);
@@ -267,6 +328,11 @@ __global__ void __launch_bounds__(kThreads, 1)
   red[quarter * kRows + r] = l_run;
   __syncthreads();
   const float l_tot = red[r] + red[kRows + r] + red[2 * kRows + r] + red[3 * kRows + r];
+  if constexpr (FP8) {  // O = s_v * (P . V8)
+    const float sv = v_scale[kvh];
+#pragma unroll
+    for (int d = 0; d < 32; ++d) o[d] *= sv;
+  }
 
   if (!failed && row_valid) {
     if (splits == 1) {
@@ -357,21 +423,25 @@ AttnPlan attention_plan(int B, int T, int H, int Hkv, int S, int num_sms) {
 int launch_attention(const void* q, const CUtensorMap* tm_k, const CUtensorMap* tm_v, void* out, float* ws,
                      const int* kv_len, const int* n_new, const int64_t* mask, int B, int T, int H, int Hkv, int D,
                      int S, float scale, int q_offset, const AttnPlan& plan, unsigned* status, cudaStream_t stream,
-                     unsigned long long* trace) {
+                     unsigned long long* trace, const float* k_scale, const float* v_scale) {
   if (D != kDim || H % Hkv != 0) return -1;
   if (mask != nullptr && T > 64) return -1;
+  const bool fp8 = k_scale != nullptr;
+  if (fp8 && v_scale == nullptr) return -1;
   static bool configured = false;
   if (!configured) {
-    cudaFuncSetAttribute(attn_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmem);
+    cudaFuncSetAttribute(attn_tc_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmem);
+    cudaFuncSetAttribute(attn_tc_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmem);
     configured = true;
   }
   const int ctas = B * Hkv * plan.m_tiles;
   float* ws_o = plan.splits > 1 ? ws : nullptr;
   float* ws_ml = plan.splits > 1 ? ws + static_cast<size_t>(ctas) * plan.splits * kRows * kDim : nullptr;
   dim3 grid(ctas, plan.splits);
-  launch_pdl(attn_tc_kernel, grid, dim3(kThreads), kSmem, stream, static_cast<const bf16*>(q), *tm_k, *tm_v,
-             static_cast<bf16*>(out), ws_o, ws_ml, kv_len, n_new, mask, T, H, Hkv, S, scale * 1.4426950408889634f,
-             q_offset, plan.chunks_per_split, plan.m_tiles, status, trace);
+  launch_pdl(fp8 ? attn_tc_kernel<true> : attn_tc_kernel<false>, grid, dim3(kThreads), kSmem, stream,
+             static_cast<const bf16*>(q), *tm_k, *tm_v, static_cast<bf16*>(out), ws_o, ws_ml, kv_len, n_new, mask, T,
+             H, Hkv, S, scale * 1.4426950408889634f, q_offset, plan.chunks_per_split, plan.m_tiles, status, trace,
+             k_scale, v_scale);
   if (plan.splits > 1) {
     dim3 mgrid(ctas, kRows / 4);
     launch_pdl(attn_merge_kernel, mgrid, dim3(128), 0, stream, static_cast<const float*>(ws_o),

@@ -134,12 +134,28 @@ std::tuple<Tensor, Tensor> rmsnorm(Tensor x, Tensor w, double eps, c10::optional
   return {out, resid_out};
 }
 
+// fp8 scales: per-KV-head fp32 [Hkv] (K = k_scale * K8, V = v_scale * V8) when the caches hold e4m3 codes.
+bool fp8_cache(const Tensor& k_cache, const c10::optional<Tensor>& k_scale, const c10::optional<Tensor>& v_scale,
+               int64_t Hkv) {
+  if (k_cache.scalar_type() == at::kBFloat16) return false;
+  TORCH_CHECK(k_cache.scalar_type() == at::kFloat8_e4m3fn, "caches must be bf16 or float8_e4m3fn");
+  TORCH_CHECK(k_scale.has_value() && v_scale.has_value(), "fp8 caches need k_scale and v_scale");
+  for (const Tensor* t : {&*k_scale, &*v_scale}) {
+    TORCH_CHECK(t->scalar_type() == at::kFloat && t->is_contiguous() && t->numel() == Hkv,
+                "fp8 scales must be contiguous fp32 [Hkv]");
+  }
+  return true;
+}
+
 Tensor rope_store(Tensor qkv, Tensor positions, Tensor cos, Tensor sin, int64_t H, int64_t Hkv, int64_t D,
                   Tensor k_cache, Tensor v_cache, Tensor kv_len, Tensor n_new, c10::optional<Tensor> q_norm,
-                  c10::optional<Tensor> k_norm, double eps, int64_t q_offset) {
+                  c10::optional<Tensor> k_norm, double eps, int64_t q_offset, c10::optional<Tensor> k_scale,
+                  c10::optional<Tensor> v_scale) {
   CHECK_CUDA(qkv);
   CHECK_BF16(qkv);
-  CHECK_BF16(k_cache);
+  TORCH_CHECK(D == 128, "rope_store: head_dim must be 128, got ", D);
+  const bool fp8 = fp8_cache(k_cache, k_scale, v_scale, Hkv);
+  TORCH_CHECK(v_cache.scalar_type() == k_cache.scalar_type(), "K and V caches must share a dtype");
   CHECK_I32(positions);
   CHECK_I32(kv_len);
   CHECK_I32(n_new);
@@ -157,17 +173,20 @@ Tensor rope_store(Tensor qkv, Tensor positions, Tensor cos, Tensor sin, int64_t 
       k_cache.data_ptr(), v_cache.data_ptr(), kv_len.data_ptr<int>(), n_new.data_ptr<int>(),
       q_norm.has_value() ? q_norm->data_ptr() : nullptr, k_norm.has_value() ? k_norm->data_ptr() : nullptr,
       static_cast<float>(eps), B, T, static_cast<int>(H), static_cast<int>(Hkv), static_cast<int>(D),
-      static_cast<int>(k_cache.size(2)), static_cast<int>(q_offset), at::cuda::getCurrentCUDAStream());
+      static_cast<int>(k_cache.size(2)), static_cast<int>(q_offset), at::cuda::getCurrentCUDAStream(),
+      fp8 ? k_scale->data_ptr<float>() : nullptr, fp8 ? v_scale->data_ptr<float>() : nullptr);
   TORCH_CHECK(rc == 0, "rope_store: unsupported head_dim ", D);
   return q;
 }
 
 Tensor attention(Tensor q, Tensor k_cache, Tensor v_cache, Tensor kv_len, Tensor n_new, c10::optional<Tensor> mask,
-                 double scale, int64_t q_offset, c10::optional<Tensor> trace) {
+                 double scale, int64_t q_offset, c10::optional<Tensor> trace, c10::optional<Tensor> k_scale,
+                 c10::optional<Tensor> v_scale) {
   CHECK_CUDA(q);
   CHECK_BF16(q);
-  CHECK_BF16(k_cache);
-  CHECK_BF16(v_cache);
+  TORCH_CHECK(q.dim() == 4 && q.size(3) == 128 && k_cache.dim() == 4, "attention: head_dim must be 128");
+  const bool fp8 = fp8_cache(k_cache, k_scale, v_scale, k_cache.size(1));
+  TORCH_CHECK(v_cache.scalar_type() == k_cache.scalar_type(), "K and V caches must share a dtype");
   CHECK_I32(kv_len);
   CHECK_I32(n_new);
   TORCH_CHECK(q.dim() == 4 && k_cache.dim() == 4, "attention expects q [B, T, H, D] and caches [B, Hkv, S, D]");
@@ -190,8 +209,10 @@ Tensor attention(Tensor q, Tensor k_cache, Tensor v_cache, Tensor kv_len, Tensor
   Tensor ws;
   if (plan.ws_floats > 0) ws = at::empty({plan.ws_floats}, q.options().dtype(at::kFloat));
   const uint64_t rows = static_cast<uint64_t>(B) * Hkv * S;
-  const CUtensorMap* tk = tensor_map(k_cache.data_ptr(), rows, D, D, 128);
-  const CUtensorMap* tv = tensor_map(v_cache.data_ptr(), rows, D, D, 128);
+  const CUtensorMap* tk = fp8 ? tensor_map_ex(k_cache.data_ptr(), 1, rows, D, D, D, 128, 0)
+                              : tensor_map(k_cache.data_ptr(), rows, D, D, 128);
+  const CUtensorMap* tv = fp8 ? tensor_map_ex(v_cache.data_ptr(), 1, rows, D, D, D, 128, 0)
+                              : tensor_map(v_cache.data_ptr(), rows, D, D, 128);
   const int rc = ecz::launch_attention(q.data_ptr(), tk, tv, out.data_ptr(),
                                        plan.ws_floats > 0 ? ws.data_ptr<float>() : nullptr, kv_len.data_ptr<int>(),
                                        n_new.data_ptr<int>(), mask_ptr, B, T, H, Hkv, D, S,
@@ -199,7 +220,9 @@ Tensor attention(Tensor q, Tensor k_cache, Tensor v_cache, Tensor kv_len, Tensor
                                        status_word(q.device()), at::cuda::getCurrentCUDAStream(),
                                        trace.has_value() ? reinterpret_cast<unsigned long long*>(
                                                                trace->data_ptr<int64_t>())
-                                                         : nullptr);
+                                                         : nullptr,
+                                       fp8 ? k_scale->data_ptr<float>() : nullptr,
+                                       fp8 ? v_scale->data_ptr<float>() : nullptr);
   TORCH_CHECK(rc == 0, "attention: unsupported shape (head_dim must be 128, H divisible by H_kv)");
   return out;
 }
@@ -337,7 +360,7 @@ std::tuple<Tensor, Tensor, Tensor> greedy_accept(Tensor tokens, Tensor parents, 
 
 void kv_compact(Tensor cache, Tensor kv_len, Tensor path, Tensor n_acc) {
   CHECK_CUDA(cache);
-  CHECK_BF16(cache);
+  TORCH_CHECK(cache.element_size() == 2 || cache.element_size() == 1, "cache must be bf16 or fp8");
   CHECK_I32(kv_len);
   CHECK_I32(path);
   CHECK_I32(n_acc);
@@ -350,7 +373,8 @@ void kv_compact(Tensor cache, Tensor kv_len, Tensor path, Tensor n_acc) {
   const int T = static_cast<int>(path.size(1));
   const int max_depth = std::max(1, T - 1);
   const int rc = ecz::launch_kv_compact(cache.data_ptr(), kv_len.data_ptr<int>(), path.data_ptr<int>(),
-                                        n_acc.data_ptr<int>(), LH, B, Hkv, S, D, T, std::min(max_depth, 64),
+                                        n_acc.data_ptr<int>(), LH, B, Hkv, S, D * static_cast<int>(cache.element_size()),
+                                        T, std::min(max_depth, 64),
                                         at::cuda::getCurrentCUDAStream());
   TORCH_CHECK(rc == 0, "kv_compact: unsupported head_dim or path length");
 }
@@ -516,14 +540,23 @@ int64_t gemm_cluster_splits(int64_t M, int64_t N, int64_t K, int64_t sms) {
 
 }  // namespace
 
+// Raises a formatted error: a host-only check that exceptions thrown in this library reach Python.
+void raise_formatted(int64_t n) { TORCH_CHECK(n < 0, "formatted error ", n, " from economize_b200._C"); }
+
 PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.doc() = "economize_b200 sm_100a kernels (tcgen05 / TMA)";
   m.def("rmsnorm", &rmsnorm, "fused residual add + RMSNorm");
-  m.def("rope_store", &rope_store, "rotary embedding + KV-cache write (+ optional QK-norm)");
-  m.def("attention", &attention, "tree-masked / causal attention over the slot cache (tcgen05)",
+  m.def("rope_store", &rope_store, "rotary embedding + KV-cache write (+ optional QK-norm; fp8 caches quantize)",
+        py::arg("qkv"), py::arg("positions"), py::arg("cos"), py::arg("sin"), py::arg("H"), py::arg("Hkv"),
+        py::arg("D"), py::arg("k_cache"), py::arg("v_cache"), py::arg("kv_len"), py::arg("n_new"), py::arg("q_norm"),
+        py::arg("k_norm"), py::arg("eps"), py::arg("q_offset"), py::arg("k_scale") = py::none(),
+        py::arg("v_scale") = py::none());
+  m.def("attention", &attention, "tree-masked / causal attention over the slot cache (tcgen05; bf16 or fp8 KV)",
         py::arg("q"), py::arg("k_cache"), py::arg("v_cache"), py::arg("kv_len"), py::arg("n_new"), py::arg("mask"),
-        py::arg("scale"), py::arg("q_offset"), py::arg("trace") = py::none());
+        py::arg("scale"), py::arg("q_offset"), py::arg("trace") = py::none(), py::arg("k_scale") = py::none(),
+        py::arg("v_scale") = py::none());
   m.def("silu_mul", &silu_mul, "SwiGLU activation of [gate; up]");
+  m.def("raise_formatted", &raise_formatted, "raise a formatted RuntimeError (exception-path self test)");
   m.def("linear", &linear, "x @ w.T on tcgen05 (swap-AB, split-K)");
   m.def("linear_wq", &linear_wq, "weight-only quantized x @ dequant(w).T (int4 / int8 / fp8 weights)", py::arg("x"),
         py::arg("qweight"), py::arg("scales"), py::arg("zeros"), py::arg("fmt"), py::arg("group"), py::arg("splits") = 0);

@@ -9,6 +9,8 @@
 //
 // Rounding follows Hugging Face's Llama modules where it matters for greedy identity: the residual sum and the
 // normalized value are rounded to bf16 before the weight multiply, and the rotary products are rounded per term.
+#include <cuda_fp8.h>
+
 #include "common.cuh"
 #include "launchers.h"
 
@@ -112,7 +114,7 @@ __global__ void __launch_bounds__(256) rope_store_kernel(
     const float* __restrict__ sin_t, bf16* __restrict__ q_out, bf16* __restrict__ k_cache,
     bf16* __restrict__ v_cache, const int* __restrict__ kv_len, const int* __restrict__ n_new,
     const bf16* __restrict__ q_norm, const bf16* __restrict__ k_norm, float eps, int tokens, int T, int H, int Hkv,
-    int S, int q_offset) {
+    int S, int q_offset, const float* __restrict__ k_scale, const float* __restrict__ v_scale) {
   pdl_trigger();
   pdl_wait();
   constexpr int D = 128;
@@ -162,6 +164,24 @@ __global__ void __launch_bounds__(256) rope_store_kernel(
   const int kvh = head - H;
   const size_t slot = static_cast<size_t>(kv_len[b]) + j;
   const size_t off = ((static_cast<size_t>(b) * Hkv + kvh) * S + slot) * D;
+  if (k_scale != nullptr) {
+    // fp8 cache: e4m3 codes of value / scale (quotient rounded to fp32 first, then to e4m3 with saturation)
+    const bf16* vsrc = qkv + static_cast<size_t>(token) * width + (H + Hkv) * D + kvh * D;
+    const float sk = k_scale[kvh], sv = v_scale[kvh];
+    uint8_t* kc = reinterpret_cast<uint8_t*>(k_cache) + off;
+    uint8_t* vc = reinterpret_cast<uint8_t*>(v_cache) + off;
+    auto put = [](uint8_t* dst, float a, float b2) {
+      *reinterpret_cast<__nv_fp8x2_storage_t*>(dst) =
+          __nv_cvt_float2_to_fp8x2(make_float2(a, b2), __NV_SATFINITE, __NV_E4M3);
+    };
+    put(kc + i0, __fdiv_rn(bf16r(r0), sk), __fdiv_rn(bf16r(r1), sk));
+    put(kc + i0 + D / 2, __fdiv_rn(bf16r(r2), sk), __fdiv_rn(bf16r(r3), sk));
+    const __nv_bfloat162 va = *reinterpret_cast<const __nv_bfloat162*>(vsrc + i0);
+    const __nv_bfloat162 vb = *reinterpret_cast<const __nv_bfloat162*>(vsrc + i0 + D / 2);
+    put(vc + i0, __fdiv_rn(__bfloat162float(va.x), sv), __fdiv_rn(__bfloat162float(va.y), sv));
+    put(vc + i0 + D / 2, __fdiv_rn(__bfloat162float(vb.x), sv), __fdiv_rn(__bfloat162float(vb.y), sv));
+    return;
+  }
   *reinterpret_cast<__nv_bfloat162*>(k_cache + off + i0) = __floats2bfloat162_rn(r0, r1);
   *reinterpret_cast<__nv_bfloat162*>(k_cache + off + i0 + D / 2) = __floats2bfloat162_rn(r2, r3);
   const bf16* vsrc = qkv + static_cast<size_t>(token) * width + (H + Hkv) * D + kvh * D;
@@ -173,14 +193,14 @@ __global__ void __launch_bounds__(256) rope_store_kernel(
 int launch_rope_store(const void* qkv, const int* positions, const float* cos_t, const float* sin_t, void* q_out,
                       void* k_cache, void* v_cache, const int* kv_len, const int* n_new, const void* q_norm,
                       const void* k_norm, float eps, int B, int T, int H, int Hkv, int D, int S, int q_offset,
-                      cudaStream_t stream) {
+                      cudaStream_t stream, const float* k_scale, const float* v_scale) {
   if (D != 128) return -1;
   const long warps = static_cast<long>(B) * T * (H + Hkv);
   const int blocks = static_cast<int>((warps * 32 + 255) / 256);
   launch_pdl(rope_store_kernel, dim3(blocks), dim3(256), 0, stream, static_cast<const bf16*>(qkv), positions, cos_t,
              sin_t, static_cast<bf16*>(q_out), static_cast<bf16*>(k_cache), static_cast<bf16*>(v_cache), kv_len,
              n_new, static_cast<const bf16*>(q_norm), static_cast<const bf16*>(k_norm), eps, B * T, T, H, Hkv, S,
-             q_offset);
+             q_offset, k_scale, v_scale);
   return 0;
 }
 
@@ -380,37 +400,38 @@ int launch_greedy_accept(const int64_t* tokens, const int64_t* parents, const in
 // One CTA per (layer*2 + kv, b, kv head); every thread reads its 16-byte chunk first, then all write, so
 // overlapping source/destination slots of one path never race.
 // ---------------------------------------------------------------------------------------------------------------
-__global__ void kv_compact_kernel(bf16* __restrict__ cache, const int* __restrict__ kv_len,
+__global__ void kv_compact_kernel(uint8_t* __restrict__ cache, const int* __restrict__ kv_len,
                                   const int* __restrict__ path, const int* __restrict__ n_acc, int B, int Hkv, int S,
-                                  int D, int T) {
+                                  int row_bytes, int T) {
   pdl_trigger();
   pdl_wait();
   const int lh = blockIdx.x;  // layer*2 + kv
   const int b = blockIdx.y, h = blockIdx.z;
   const int n = n_acc[b];
-  const int vecs = D / 8;
+  const int vecs = row_bytes / 16;
   const int i = threadIdx.x / vecs + 1;  // path position (the root at 0 never moves)
   const int c = threadIdx.x % vecs;
-  bf16* base = cache + ((static_cast<size_t>(lh) * B + b) * Hkv + h) * static_cast<size_t>(S) * D;
+  uint8_t* base = cache + ((static_cast<size_t>(lh) * B + b) * Hkv + h) * static_cast<size_t>(S) * row_bytes;
   const int start = kv_len[b];
   uint4 v = make_uint4(0, 0, 0, 0);
   const bool active = i <= n && i < T;
   int src = 0;
   if (active) {
     src = path[static_cast<size_t>(b) * T + i];
-    v = reinterpret_cast<const uint4*>(base + static_cast<size_t>(start + src) * D)[c];
+    v = reinterpret_cast<const uint4*>(base + static_cast<size_t>(start + src) * row_bytes)[c];
   }
   __syncthreads();
-  if (active && src != i) reinterpret_cast<uint4*>(base + static_cast<size_t>(start + i) * D)[c] = v;
+  if (active && src != i) reinterpret_cast<uint4*>(base + static_cast<size_t>(start + i) * row_bytes)[c] = v;
 }
 
+// Rows of `row_bytes` bytes (D * element size: bf16 and fp8 caches alike).
 int launch_kv_compact(void* cache, const int* kv_len, const int* path, const int* n_acc, int LH, int B, int Hkv,
-                      int S, int D, int T, int max_depth, cudaStream_t stream) {
-  const int threads = max_depth * (D / 8);
-  if (threads > 1024 || D % 8) return -1;
+                      int S, int row_bytes, int T, int max_depth, cudaStream_t stream) {
+  const int threads = max_depth * (row_bytes / 16);
+  if (threads > 1024 || row_bytes % 16) return -1;
   dim3 grid(LH, B, Hkv);
-  launch_pdl(kv_compact_kernel, grid, dim3(threads), 0, stream, static_cast<bf16*>(cache), kv_len, path, n_acc, B,
-             Hkv, S, D, T);
+  launch_pdl(kv_compact_kernel, grid, dim3(threads), 0, stream, static_cast<uint8_t*>(cache), kv_len, path, n_acc,
+             B, Hkv, S, row_bytes, T);
   return 0;
 }
 

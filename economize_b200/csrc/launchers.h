@@ -35,7 +35,7 @@ int launch_rmsnorm(const void* x, const void* resid, const void* w, void* out, v
 int launch_rope_store(const void* qkv, const int* positions, const float* cos_t, const float* sin_t, void* q_out,
                       void* k_cache, void* v_cache, const int* kv_len, const int* n_new, const void* q_norm,
                       const void* k_norm, float eps, int B, int T, int H, int Hkv, int D, int S, int q_offset,
-                      cudaStream_t stream);
+                      cudaStream_t stream, const float* k_scale = nullptr, const float* v_scale = nullptr);
 int launch_silu_mul(const void* gu, void* out, int rows, int F, cudaStream_t stream);
 int argmax_slices(int rows, int V);
 int launch_argmax(const void* x, bool is_bf16, int64_t* out, float* part_v, int* part_i, int rows, int V,
@@ -44,7 +44,7 @@ int launch_argmax(const void* x, bool is_bf16, int64_t* out, float* part_v, int*
 int launch_greedy_accept(const int64_t* tokens, const int64_t* parents, const int64_t* pred, const uint8_t* ok,
                          int* n_acc, int* path, int64_t* out, int B, int T, cudaStream_t stream);
 int launch_kv_compact(void* cache, const int* kv_len, const int* path, const int* n_acc, int LH, int B, int Hkv,
-                      int S, int D, int T, int max_depth, cudaStream_t stream);
+                      int S, int row_bytes, int T, int max_depth, cudaStream_t stream);
 
 // gemm_tc.cu
 int gemm_block_n(int M);
@@ -72,7 +72,8 @@ AttnPlan attention_plan(int B, int T, int H, int Hkv, int S, int num_sms);
 int launch_attention(const void* q, const CUtensorMap* tm_k, const CUtensorMap* tm_v, void* out, float* ws,
                      const int* kv_len, const int* n_new, const int64_t* mask, int B, int T, int H, int Hkv, int D,
                      int S, float scale, int q_offset, const AttnPlan& plan, unsigned* status, cudaStream_t stream,
-                     unsigned long long* trace = nullptr);
+                     unsigned long long* trace = nullptr, const float* k_scale = nullptr,
+                     const float* v_scale = nullptr);
 
 // sampling.cu
 int launch_sample(const float* probs, const float* u, int64_t* out, int rows, int V, cudaStream_t stream);

@@ -77,6 +77,9 @@ class CausalLM(nn.Module):
         self._rope: tuple[torch.Tensor, torch.Tensor] | None = None
         #: calibration hook ``observer(layer, name, x)`` called with the input of every projection (or None)
         self.observer = None
+        #: KV-cache storage set by KV techniques: dtype (None: the compute dtype) and fp8 scales ([L, H_kv] x 2)
+        self.kv_dtype: torch.dtype | None = None
+        self.kv_scales: tuple[torch.Tensor, torch.Tensor] | None = None
         #: tensor-parallel group (set by economize_b200.parallel.tp.shard_model) and this rank's shard sizes
         self.tp = None
         self.local = dict(num_heads=config.num_heads, num_kv_heads=config.num_kv_heads,
@@ -107,9 +110,12 @@ class CausalLM(nn.Module):
         return self._rope
 
     def new_cache(self, batch: int, capacity: int) -> KVCache:
+        """A zeroed cache in the model's KV format (``kv_dtype``: the compute dtype, or fp8 e4m3 with the per-head
+        ``kv_scales`` a KV technique set)."""
         c = self.config
-        return KVCache(c.num_layers, batch, self.local["num_kv_heads"], capacity, c.head_dim, self.dtype,
-                       self.device)
+        dtype = self.kv_dtype or self.dtype
+        return KVCache(c.num_layers, batch, self.local["num_kv_heads"], capacity, c.head_dim, dtype, self.device,
+                       self.kv_scales)
 
     @property
     def tp_size(self) -> int:
@@ -169,11 +175,13 @@ class CausalLM(nn.Module):
             self.observer(index, "wqkv", x)
         qkv = ops.linear(x, layer.wqkv, layer.bqkv)
         k_cache, v_cache = cache.layer(index)
+        k_scale, v_scale = cache.layer_scales(index)
         q = ops.rope_store(qkv, batch.positions, cos, sin, self.local["num_heads"], self.local["num_kv_heads"],
                            c.head_dim, k_cache,
                            v_cache, batch.kv_len, batch.n_new, layer.q_norm, layer.k_norm, c.rms_norm_eps,
-                           q_offset=batch.q_offset)
-        o = ops.attention(q, k_cache, v_cache, batch.kv_len, batch.n_new, batch.mask, q_offset=batch.q_offset)
+                           q_offset=batch.q_offset, k_scale=k_scale, v_scale=v_scale)
+        o = ops.attention(q, k_cache, v_cache, batch.kv_len, batch.n_new, batch.mask, q_offset=batch.q_offset,
+                          k_scale=k_scale, v_scale=v_scale)
         o = o.reshape(*o.shape[:2], -1)
         if self.observer is not None:
             self.observer(index, "wo", o)

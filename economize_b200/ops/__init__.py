@@ -43,24 +43,29 @@ def rmsnorm(x: torch.Tensor, weight: torch.Tensor, eps: float,
 def rope_store(qkv: torch.Tensor, positions: torch.Tensor, cos: torch.Tensor, sin: torch.Tensor, num_heads: int,
                num_kv_heads: int, head_dim: int, k_cache: torch.Tensor, v_cache: torch.Tensor,
                kv_len: torch.Tensor, n_new: torch.Tensor, q_norm: torch.Tensor | None = None,
-               k_norm: torch.Tensor | None = None, eps: float = 1e-6, q_offset: int = 0) -> torch.Tensor:
+               k_norm: torch.Tensor | None = None, eps: float = 1e-6, q_offset: int = 0,
+               k_scale: torch.Tensor | None = None, v_scale: torch.Tensor | None = None) -> torch.Tensor:
     """Fused (per-head RMSNorm +) rotary embedding of queries and keys and the KV-cache write (see
-    :func:`.reference.rope_store`)."""
+    :func:`.reference.rope_store`); fp8 caches are written as e4m3 codes of ``value / scale``."""
     if qkv.is_cuda:
         return require().rope_store(qkv, positions, cos, sin, num_heads, num_kv_heads, head_dim, k_cache, v_cache,
-                                    kv_len, n_new, q_norm, k_norm, float(eps), int(q_offset))
+                                    kv_len, n_new, q_norm, k_norm, float(eps), int(q_offset), k_scale, v_scale)
     return reference.rope_store(qkv, positions, cos, sin, num_heads, num_kv_heads, head_dim, k_cache, v_cache,
-                                kv_len, n_new, q_norm, k_norm, eps, q_offset)
+                                kv_len, n_new, q_norm, k_norm, eps, q_offset, k_scale, v_scale)
 
 
 def attention(q: torch.Tensor, k_cache: torch.Tensor, v_cache: torch.Tensor, kv_len: torch.Tensor,
               n_new: torch.Tensor, mask: torch.Tensor | None = None, scale: float | None = None,
-              q_offset: int = 0) -> torch.Tensor:
-    """Causal / tree-masked attention over the slot cache (see :func:`.reference.attention`)."""
+              q_offset: int = 0, k_scale: torch.Tensor | None = None,
+              v_scale: torch.Tensor | None = None) -> torch.Tensor:
+    """Causal / tree-masked attention over the slot cache (see :func:`.reference.attention`); fp8 caches take
+    per-KV-head scales."""
     scale = float(scale if scale is not None else q.shape[-1] ** -0.5)
     if q.is_cuda:
-        return require().attention(q, k_cache, v_cache, kv_len, n_new, mask, scale, int(q_offset))
-    return reference.attention(q, k_cache, v_cache, kv_len, n_new, mask, scale, q_offset=q_offset)
+        return require().attention(q, k_cache, v_cache, kv_len, n_new, mask, scale, int(q_offset), None, k_scale,
+                                   v_scale)
+    return reference.attention(q, k_cache, v_cache, kv_len, n_new, mask, scale, q_offset=q_offset, k_scale=k_scale,
+                               v_scale=v_scale)
 
 
 def silu_mul(gate_up: torch.Tensor) -> torch.Tensor:

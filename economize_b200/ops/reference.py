@@ -46,10 +46,12 @@ def _rotate(x: torch.Tensor, cos: torch.Tensor, sin: torch.Tensor) -> torch.Tens
 def rope_store(qkv: torch.Tensor, positions: torch.Tensor, cos: torch.Tensor, sin: torch.Tensor, num_heads: int,
                num_kv_heads: int, head_dim: int, k_cache: torch.Tensor, v_cache: torch.Tensor,
                kv_len: torch.Tensor, n_new: torch.Tensor, q_norm: torch.Tensor | None = None,
-               k_norm: torch.Tensor | None = None, eps: float = 1e-6, q_offset: int = 0) -> torch.Tensor:
+               k_norm: torch.Tensor | None = None, eps: float = 1e-6, q_offset: int = 0,
+               k_scale: torch.Tensor | None = None, v_scale: torch.Tensor | None = None) -> torch.Tensor:
     """Rotate queries and keys of ``qkv [B, T, (H + 2 H_kv) D]`` (optionally after a per-head RMSNorm), write the keys
     and values of token ``t`` to cache slot ``kv_len[b] + q_offset + t`` of ``k_cache/v_cache [B, H_kv, S, D]`` when
-    ``q_offset + t < n_new[b]``, and return the rotated queries ``[B, T, H, D]``."""
+    ``q_offset + t < n_new[b]``, and return the rotated queries ``[B, T, H, D]``. fp8 caches store
+    ``e4m3(value / scale)`` with one fp32 scale per KV head (``k_scale``, ``v_scale`` ``[H_kv]``)."""
     batch, length, _ = qkv.shape
     q, k, v = qkv.split([num_heads * head_dim, num_kv_heads * head_dim, num_kv_heads * head_dim], -1)
     q = q.reshape(batch, length, num_heads, head_dim)
@@ -62,6 +64,9 @@ def rope_store(qkv: torch.Tensor, positions: torch.Tensor, cos: torch.Tensor, si
     pos = positions.long()
     c, s = cos[pos][:, :, None], sin[pos][:, :, None]  # [B, T, 1, D/2]
     q, k = _rotate(q, c, s), _rotate(k, c, s)
+    if k_cache.dtype == torch.float8_e4m3fn:
+        k = (k.to(torch.bfloat16).float() / k_scale.float()[:, None]).clamp(-448, 448)
+        v = (v.to(torch.bfloat16).float() / v_scale.float()[:, None]).clamp(-448, 448)
     for b in range(batch):
         n, start = min(int(n_new[b]) - q_offset, length), int(kv_len[b]) + q_offset
         if n > 0:
@@ -91,8 +96,10 @@ def visible_mask(kv_len: torch.Tensor, n_new: torch.Tensor, length: int, width: 
 
 def attention(q: torch.Tensor, k_cache: torch.Tensor, v_cache: torch.Tensor, kv_len: torch.Tensor,
               n_new: torch.Tensor, mask: torch.Tensor | None = None, scale: float | None = None,
-              softcap: float | None = None, q_offset: int = 0) -> torch.Tensor:
-    """Attention of queries ``[B, T, H, D]`` over the slot cache ``[B, H_kv, S, D]``.
+              softcap: float | None = None, q_offset: int = 0, k_scale: torch.Tensor | None = None,
+              v_scale: torch.Tensor | None = None) -> torch.Tensor:
+    """Attention of queries ``[B, T, H, D]`` over the slot cache ``[B, H_kv, S, D]`` (bf16, fp32, or e4m3 codes with
+    per-KV-head scales ``k_scale``/``v_scale``).
 
     Query ``t`` of row ``b`` sees every committed slot ``< kv_len[b]`` and the new tokens' slots ``kv_len[b] + j``
     (``j < n_new[b]``) for which bit ``j`` of ``mask[b, t]`` is set (``mask=None``: causal, ``j <= q_offset + t``).
@@ -104,6 +111,9 @@ def attention(q: torch.Tensor, k_cache: torch.Tensor, v_cache: torch.Tensor, kv_
     vis = visible_mask(kv_len, n_new, length, width, mask, q_offset)  # [B, T, W]
     keys = k_cache[:, :, :width].float()
     values = v_cache[:, :, :width].float()
+    if k_scale is not None:
+        keys = keys * k_scale.float()[None, :, None, None]
+        values = values * v_scale.float()[None, :, None, None]
     group = heads // kv_heads
     keys = keys.repeat_interleave(group, 1)
     values = values.repeat_interleave(group, 1)
@@ -181,6 +191,8 @@ def greedy_accept(tokens: torch.Tensor, parents: torch.Tensor, pred: torch.Tenso
 def kv_compact(cache: torch.Tensor, kv_len: torch.Tensor, path: torch.Tensor, n_acc: torch.Tensor) -> None:
     """Move the cache entries of an accepted tree path to consecutive slots: slot ``kv_len + path[b, i]`` to
     ``kv_len + i`` for ``i <= n_acc[b]``, in every layer of ``cache [L, 2, B, H_kv, S, D]``."""
+    if cache.dtype == torch.float8_e4m3fn:
+        cache = cache.view(torch.uint8)
     for b in range(cache.shape[2]):
         n, base = int(n_acc[b]), int(kv_len[b])
         src = base + path[b, : n + 1].long()

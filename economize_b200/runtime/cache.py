@@ -20,15 +20,31 @@ __all__ = ["KVCache", "StepBatch"]
 
 
 class KVCache:
-    """Keys and values of ``num_layers`` layers for ``batch`` rows of ``capacity`` slots."""
+    """Keys and values of ``num_layers`` layers for ``batch`` rows of ``capacity`` slots.
+
+    ``dtype=torch.float8_e4m3fn`` stores e4m3 codes with one static fp32 scale per (layer, KV head): ``scales`` is
+    ``(k_scale, v_scale)``, each ``[L, H_kv]`` (economize's ``kv_fp8`` with per-head scales instead of its
+    ``none/token/tensor`` modes, ``src/economize/techniques/kv_quant/fp8.py:55-270``)."""
 
     def __init__(self, num_layers: int, batch: int, num_kv_heads: int, capacity: int, head_dim: int,
-                 dtype: torch.dtype, device: torch.device | str) -> None:
+                 dtype: torch.dtype, device: torch.device | str,
+                 scales: tuple[torch.Tensor, torch.Tensor] | None = None) -> None:
         self.num_layers, self.batch, self.capacity = num_layers, batch, capacity
         self.data = torch.zeros(num_layers, 2, batch, num_kv_heads, capacity, head_dim, dtype=dtype, device=device)
+        self.scales = None
+        if dtype == torch.float8_e4m3fn:
+            if scales is None:
+                ones = torch.ones(num_layers, num_kv_heads, dtype=torch.float32, device=device)
+                scales = (ones, ones.clone())
+            self.scales = tuple(s.to(device=device, dtype=torch.float32).contiguous() for s in scales)
 
     def layer(self, index: int) -> tuple[torch.Tensor, torch.Tensor]:
         return self.data[index, 0], self.data[index, 1]
+
+    def layer_scales(self, index: int) -> tuple[torch.Tensor | None, torch.Tensor | None]:
+        if self.scales is None:
+            return None, None
+        return self.scales[0][index], self.scales[1][index]
 
     @property
     def nbytes(self) -> int:

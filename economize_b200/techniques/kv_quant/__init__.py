@@ -1,0 +1,127 @@
+"""KV-cache quantization: ``kv_fp8`` / ``kv_fp8_fused`` (e4m3 codes with static per-head, per-layer or unit scales,
+read directly by the tcgen05 attention kernel) (economize ``techniques/kv_quant/fp8.py:55-270`` and
+``techniques/kv_fp8_fused``).
+
+The cache stores ``e4m3(x / s)``; the attention kernel converts the codes to bf16 in shared memory and applies
+``s_k`` to the scores and ``s_v`` to the output, so a decode pass reads half the cache bytes. Scales come from the
+absolute maxima of a calibration prefill (``scale="head"``: one per layer and KV head, ``"tensor"``: one per layer,
+``"none"``: 1.0) divided by 448, e4m3's largest finite value.
+"""
+
+from __future__ import annotations
+
+from dataclasses import dataclass
+from typing import Any, ClassVar
+
+import torch
+
+from ...core.technique import Capability, Family, Technique, TechniqueConfig, register_technique
+from ...errors import ConfigError
+from ...validation import check_choice
+
+__all__ = ["KVFp8Config", "KVFp8FusedConfig", "KVFp8Technique", "calibrate_kv_scales"]
+
+E4M3_MAX = 448.0
+
+
+@dataclass(frozen=True)
+class KVFp8Config(TechniqueConfig):
+    """fp8 KV cache.
+
+    Args:
+        format: ``"e4m3"`` (the only format the kernels read).
+        scale: ``"head"`` (static per layer and KV head, from calibration), ``"tensor"`` (one per layer) or
+            ``"none"`` (unit scales: values beyond +-448 saturate).
+        margin: Headroom factor applied to calibrated maxima.
+    """
+
+    technique: ClassVar[str] = "kv_fp8"
+    format: str = "e4m3"
+    scale: str = "head"
+    margin: float = 1.0
+
+    def __post_init__(self) -> None:
+        check_choice("format", self.format, ("e4m3",))
+        check_choice("scale", self.scale, ("head", "tensor", "none"))
+        if self.margin < 1.0:
+            raise ConfigError("margin must be >= 1")
+
+
+@dataclass(frozen=True)
+class KVFp8FusedConfig(KVFp8Config):
+    """Same storage under economize's name for the kernel-read fp8 views."""
+
+    technique: ClassVar[str] = "kv_fp8_fused"
+
+
+@torch.no_grad()
+def calibrate_kv_scales(model, batches, mode: str = "head", margin: float = 1.0) -> tuple[torch.Tensor, torch.Tensor]:
+    """Per (layer, KV head) scales ``max|x| * margin / 448`` of keys (after rotary) and values over a prefill of the
+    calibration token batches ``[B, L]``."""
+    from ...runtime.cache import KVCache, StepBatch
+
+    c = model.config
+    hkv = model.local["num_kv_heads"]
+    amax = torch.zeros(2, c.num_layers, hkv, device=model.device)
+    for tokens in batches:
+        tokens = torch.as_tensor(tokens).to(model.device)
+        if tokens.dim() == 1:
+            tokens = tokens[None]
+        b, length = tokens.shape
+        cache = KVCache(c.num_layers, b, hkv, ((length + 127) // 128) * 128, c.head_dim, model.dtype, model.device)
+        lengths = torch.full((b,), length, dtype=torch.int32, device=model.device)
+        model.forward_step(tokens, StepBatch.prefill(lengths, length), cache)
+        vals = cache.data[:, :, :, :, :length].float().abs().amax(dim=(2, 4, 5))  # [L, 2, Hkv]
+        amax = torch.maximum(amax, vals.permute(1, 0, 2))
+    if mode == "tensor":
+        amax = amax.amax(-1, keepdim=True).expand_as(amax)
+    scales = torch.where(amax > 0, amax * margin / E4M3_MAX, torch.ones_like(amax))
+    return scales[0].contiguous(), scales[1].contiguous()
+
+
+@register_technique
+class KVFp8Technique(Technique):
+    config_class = KVFp8Config
+    capabilities = Capability.KV_CACHE
+    family = Family.KV_COMPRESSION
+    lossless = False
+
+    def __init__(self, config: KVFp8Config, model) -> None:
+        super().__init__(config, model)
+        hkv = model.local["num_kv_heads"]
+        ones = torch.ones(model.config.num_layers, hkv, dtype=torch.float32, device=model.device)
+        self.register_buffer("k_scale", ones.clone())
+        self.register_buffer("v_scale", ones.clone())
+        self._calibration: Any = None
+        self._calibrated = False
+
+    def calibrate(self, calibration: Any) -> None:
+        self._calibration = calibration
+
+    def load_technique_state(self, state: dict[str, torch.Tensor]) -> None:
+        super().load_technique_state(state)
+        self._calibrated = True
+
+    def attach(self) -> None:
+        model = self.model
+        if not self._calibrated and self.config.scale != "none":
+            if self._calibration is None:
+                raise ConfigError(f"kv_fp8 with scale={self.config.scale!r} needs calibration tokens "
+                                  "(apply(..., calibration=ids)); use scale='none' for unit scales")
+            cal = self._calibration
+            batches = [cal] if isinstance(cal, torch.Tensor) else list(cal)
+            k, v = calibrate_kv_scales(model, batches, self.config.scale, self.config.margin)
+            self.k_scale.copy_(k)
+            self.v_scale.copy_(v)
+            self._calibrated = True
+        model.kv_dtype = torch.float8_e4m3fn
+        model.kv_scales = (self.k_scale, self.v_scale)
+
+    def detach(self) -> None:
+        self.model.kv_dtype = None
+        self.model.kv_scales = None
+
+
+@register_technique
+class KVFp8FusedTechnique(KVFp8Technique):
+    config_class = KVFp8FusedConfig

@@ -7,10 +7,20 @@ from setuptools import find_packages, setup
 from torch.utils.cpp_extension import BuildExtension, CUDAExtension
 
 HERE = os.path.dirname(os.path.abspath(__file__))
+
+# Build with the distribution's compiler (host code of the .cu files included; ECZ_HOST_CXX overrides). A GCC
+# wrapper that images put into CC/CXX links shared objects in which a C++ exception thrown by the extension (every
+# TORCH_CHECK that formats its message) crashes the process instead of raising a Python error.
+HOST_CXX = os.environ.get("ECZ_HOST_CXX", "/usr/bin/g++")
+if os.path.exists(HOST_CXX):
+    os.environ["CXX"] = HOST_CXX
+    os.environ["CC"] = HOST_CXX.replace("g++", "gcc") if os.path.exists(HOST_CXX.replace("g++", "gcc")) else HOST_CXX
+    os.environ["LDSHARED"] = HOST_CXX + " -shared"
 CSRC = os.path.join(HERE, "economize_b200", "csrc")
 
 NVCC_FLAGS = [
     "-gencode", "arch=compute_100a,code=sm_100a",
+    *(["-ccbin", HOST_CXX] if os.path.exists(HOST_CXX) else []),
     "-O3", "-lineinfo", "-std=c++17",
     "--expt-relaxed-constexpr",
     "-Xptxas", "-v" if os.environ.get("ECZ_PTXAS_VERBOSE") else "-O3",

@@ -39,3 +39,9 @@ def reference_greedy(model: CausalLM, prompt: torch.Tensor, n: int) -> torch.Ten
         out.append(tok)
         seq = torch.cat([seq, torch.tensor([tok])])
     return torch.tensor(out)
+
+
+def gpu_tiny_model(device, seed: int = 0) -> CausalLM:
+    """A tiny bf16 model the CUDA kernels accept (head_dim 128, widths multiples of 64)."""
+    cfg = tiny_llama(hidden_size=512, head_dim=128, num_heads=4, num_kv_heads=2, intermediate_size=1024)
+    return init_weights(CausalLM(cfg, torch.bfloat16, device), seed=seed)

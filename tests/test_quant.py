@@ -11,7 +11,7 @@ from economize_b200.techniques.eagle3 import Eagle3Config
 from economize_b200.techniques.quant import DraftQuantConfig, QuantConfig, gptq, rtn
 from economize_b200.techniques.quant.methods import collect
 
-from .helpers import prompts, reference_greedy, tiny_model
+from .helpers import gpu_tiny_model, prompts, reference_greedy, tiny_model
 
 
 @pytest.mark.parametrize("fmt", ["int4", "int8", "fp8"])
@@ -159,10 +159,7 @@ def test_linear_wq_splits(cuda, splits):
 
 @pytest.mark.gpu
 def test_quantized_model_decodes_on_gpu(cuda):
-    from economize_b200.models.config import tiny_llama
-    from economize_b200.models.llama import CausalLM, init_weights
-
-    model = init_weights(CausalLM(tiny_llama(), torch.bfloat16, cuda), seed=0)
+    model = gpu_tiny_model(cuda)
     eff = eco.apply(model, QuantConfig(format="int4", method="rtn", group_size=128), Eagle3Config(),
                     decoding=eco.DecodeConfig(cycle_length=4))
     p = prompts((17,))[0].to(cuda)
