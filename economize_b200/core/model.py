@@ -228,12 +228,12 @@ def build_model(model: nn.Module, configs: Sequence[TechniqueConfig], *, decodin
         if hasattr(t, "calibrate") and calibration is not None:
             t.calibrate(calibration)
         t.attach()
-    for t in techniques:  # drafter-only weight transforms act once the drafter exists
-        if hasattr(t, "quantize_drafter"):
+    for t in techniques:  # drafter transforms (draft_quant, frspec) act once the drafter is attached
+        if hasattr(t, "after_drafter"):
             drafter = next((d for d in techniques if Capability.DRAFTER in d.capabilities), None)
             if drafter is None:
-                raise ConfigError(f"{t.name} quantizes a drafter, but no drafting technique is applied")
-            t.quantize_drafter(drafter)
+                raise ConfigError(f"{t.name} transforms a drafter, but no drafting technique is applied")
+            t.after_drafter(drafter)
     if decoding is None:
         decoding = next((d for t in techniques if (d := t.default_decoding()) is not None), None)
     if decoding is None:

@@ -315,6 +315,54 @@ Tensor linear_wq(Tensor x, Tensor qweight, Tensor scales, c10::optional<Tensor> 
   return y;
 }
 
+// Explicit GEMM variant (tuning and benchmarks): mode 1 cluster split-K (DSMEM reduction), 2 split-K through a
+// global fp32 workspace reduced by the tile's last CTA, 3 persistent stream-K; splits <= 0 picks the default.
+Tensor linear_variant(Tensor x, Tensor w, int64_t mode, int64_t splits) {
+  CHECK_CUDA(x);
+  CHECK_BF16(x);
+  CHECK_BF16(w);
+  TORCH_CHECK(x.dim() == 2 && w.dim() == 2 && x.size(1) == w.size(1), "linear expects x [M, K] and w [N, K]");
+  c10::cuda::CUDAGuard guard(x.device());
+  x = x.contiguous();
+  w = w.contiguous();
+  const int M = static_cast<int>(x.size(0)), K = static_cast<int>(x.size(1)), N = static_cast<int>(w.size(0));
+  auto y = at::empty({M, N}, x.options());
+  if (M == 0) return y;
+  const int bn = ecz::gemm_block_n(M);
+  const int sms = num_sms(x.get_device());
+  const CUtensorMap* tw = tensor_map(w.data_ptr(), N, K, K, 128);
+  const CUtensorMap* tx = tensor_map(x.data_ptr(), M, K, K, bn);
+  cudaStream_t stream = at::cuda::getCurrentCUDAStream();
+  int rc = -1;
+  if (mode == 1) {
+    const int sp = splits > 0 ? static_cast<int>(splits) : ecz::gemm_cluster_splits(M, N, K, sms);
+    rc = ecz::launch_gemm_cluster(tw, tx, y.data_ptr(), M, N, K, sp, status_word(x.device()), stream);
+  } else if (mode == 2) {
+    const int sp = splits > 0 ? static_cast<int>(splits) : ecz::gemm_splits(M, N, K, sms);
+    auto ws = at::empty({static_cast<int64_t>(sp) * M * N}, x.options().dtype(at::kFloat));
+    rc = ecz::launch_gemm_bf16(tw, tx, y.data_ptr(), ws.data_ptr<float>(), M, N, K, sp, status_word(x.device()),
+                               stream, split_counters(x.device(), stream));
+  } else if (mode >= 4 && mode <= 6) {
+    // 4: two CTAs per SM, fp32 partials left in a workspace (GEMM part only); 5: same + separate reduce kernel;
+    // 6: two CTAs per SM with the in-kernel last-CTA reduction
+    const int sp = splits > 0 ? static_cast<int>(splits) : ecz::gemm_splits(M, N, K, 2 * sms);
+    auto ws = at::empty({static_cast<int64_t>(sp) * M * N}, x.options().dtype(at::kFloat));
+    rc = ecz::launch_gemm_bf16(tw, tx, y.data_ptr(), ws.data_ptr<float>(), M, N, K, sp, status_word(x.device()),
+                               stream, mode == 6 ? split_counters(x.device(), stream) : nullptr, nullptr,
+                               mode == 4 ? 3 : 1);
+  } else if (mode == 3) {
+    auto ws = at::empty({ecz::gemm_persistent_ws_floats(M, N, K, sms)}, x.options().dtype(at::kFloat));
+    rc = ecz::launch_gemm_persistent(tw, tx, y.data_ptr(), ws.data_ptr<float>(), split_counters(x.device(), stream),
+                                     M, N, K, sms, status_word(x.device()), stream);
+  }
+  TORCH_CHECK(rc == 0, "linear_variant: mode ", mode, " failed (", rc, ")");
+  return y;
+}
+
+int64_t gemm_cluster_capacity(int64_t M, int64_t splits) {
+  return ecz::gemm_cluster_capacity(static_cast<int>(M), static_cast<int>(splits));
+}
+
 Tensor argmax(Tensor x) {
   CHECK_CUDA(x);
   TORCH_CHECK(x.scalar_type() == at::kBFloat16 || x.scalar_type() == at::kFloat, "argmax takes bf16 or fp32");
@@ -556,6 +604,8 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
         py::arg("scale"), py::arg("q_offset"), py::arg("trace") = py::none(), py::arg("k_scale") = py::none(),
         py::arg("v_scale") = py::none());
   m.def("silu_mul", &silu_mul, "SwiGLU activation of [gate; up]");
+  m.def("linear_variant", &linear_variant, "x @ w.T through an explicit GEMM variant (tuning)");
+  m.def("gemm_cluster_capacity", &gemm_cluster_capacity, "resident clusters of the split-K cluster GEMM");
   m.def("raise_formatted", &raise_formatted, "raise a formatted RuntimeError (exception-path self test)");
   m.def("linear", &linear, "x @ w.T on tcgen05 (swap-AB, split-K)");
   m.def("linear_wq", &linear_wq, "weight-only quantized x @ dequant(w).T (int4 / int8 / fp8 weights)", py::arg("x"),

@@ -63,12 +63,12 @@ __device__ __forceinline__ void push_signal(const PeerOut& peer, bool wrote, uns
   }
 }
 
-template <int BN>
-__global__ void __launch_bounds__(128, 1)
+template <int BN, int OCC = 1>
+__global__ void __launch_bounds__(128, OCC)
     gemm_swapab_kernel(const __grid_constant__ CUtensorMap tm_w, const __grid_constant__ CUtensorMap tm_x,
                        bf16* __restrict__ y, float* __restrict__ ws, int* __restrict__ counters, int M, int N,
                        int K, int kb_per_split, unsigned* status, PeerOut peer) {
-  using Cfg = GemmCfg<BN>;
+  using Cfg = GemmCfg<BN, OCC>;
   constexpr int S = Cfg::kStages;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -269,22 +269,34 @@ __global__ void __launch_bounds__(256) splitk_reduce_kernel(const float* __restr
   }
 }
 
+// flags: bit 0 = two CTAs per SM for skinny tiles, bit 1 = leave the fp32 partials in ws (no reduction)
 template <int BN>
 int run_gemm(const CUtensorMap& tm_w, const CUtensorMap& tm_x, void* y, float* ws, int* counters, int M, int N,
-             int K, int splits, unsigned* status, cudaStream_t stream, const PeerOut& peer) {
-  using Cfg = GemmCfg<BN>;
+             int K, int splits, unsigned* status, cudaStream_t stream, const PeerOut& peer, int flags = 0) {
+  constexpr int kOcc2 = split_occupancy<BN>();
+  const bool occ2 = (flags & 1) != 0 && kOcc2 == 2;
   static bool configured = false;
   if (!configured) {
-    cudaFuncSetAttribute(gemm_swapab_kernel<BN>, cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg::kSmem);
+    cudaFuncSetAttribute(gemm_swapab_kernel<BN, 1>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                         GemmCfg<BN, 1>::kSmem);
+    cudaFuncSetAttribute(gemm_swapab_kernel<BN, kOcc2>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                         GemmCfg<BN, kOcc2>::kSmem);
     configured = true;
   }
   const int total_kb = (K + kBK - 1) / kBK;
   const int kbps = (total_kb + splits - 1) / splits;
   splits = (total_kb + kbps - 1) / kbps;  // no empty split
   dim3 grid((N + kBM - 1) / kBM, (M + BN - 1) / BN, splits);
-  launch_pdl(gemm_swapab_kernel<BN>, grid, dim3(128), Cfg::kSmem, stream, tm_w, tm_x, static_cast<bf16*>(y),
-             splits > 1 ? ws : nullptr, splits > 1 ? counters : nullptr, M, N, K, kbps, status, peer);
-  if (splits > 1 && counters == nullptr) {
+  if (occ2) {
+    launch_pdl(gemm_swapab_kernel<BN, kOcc2>, grid, dim3(128), GemmCfg<BN, kOcc2>::kSmem, stream, tm_w, tm_x,
+               static_cast<bf16*>(y), splits > 1 ? ws : nullptr, splits > 1 ? counters : nullptr, M, N, K, kbps,
+               status, peer);
+  } else {
+    launch_pdl(gemm_swapab_kernel<BN, 1>, grid, dim3(128), GemmCfg<BN, 1>::kSmem, stream, tm_w, tm_x,
+               static_cast<bf16*>(y), splits > 1 ? ws : nullptr, splits > 1 ? counters : nullptr, M, N, K, kbps,
+               status, peer);
+  }
+  if (splits > 1 && counters == nullptr && (flags & 2) == 0) {
     const long total = static_cast<long>(M) * N;
     const int blocks = static_cast<int>(std::min<long>((total / 4 + 255) / 256, 148L * 8));
     launch_pdl(splitk_reduce_kernel, dim3(std::max(blocks, 1)), dim3(256), 0, stream,
@@ -750,6 +762,46 @@ int gemm_cluster_splits(int M, int N, int K, int num_sms) {
   return std::min(8, gemm_splits(M, N, K, slots));
 }
 
+// How many clusters of `splits` CTAs of the BN-wide cluster kernel can be resident at once (the hardware packs
+// clusters inside GPCs, so this is far below SMs * CTAs-per-SM / splits for large clusters).
+template <int BN>
+int cluster_capacity_bn(int splits) {
+  using Cfg = GemmCfg<BN, split_occupancy<BN>()>;
+  static int cache[9] = {0};
+  if (splits < 1 || splits > 8) return 0;
+  if (cache[splits] == 0) {
+    cudaFuncSetAttribute(gemm_cluster_kernel<BN>, cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg::kSmem);
+    cudaFuncSetAttribute(gemm_cluster_kernel<BN>, cudaFuncAttributeNonPortableClusterSizeAllowed, 0);
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(splits, 1, splits);
+    cfg.blockDim = dim3(128);
+    cfg.dynamicSmemBytes = Cfg::kSmem;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = 1;
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = splits;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    int n = 0;
+    if (cudaOccupancyMaxActiveClusters(&n, gemm_cluster_kernel<BN>, &cfg) != cudaSuccess) {
+      cudaGetLastError();
+      n = 1;
+    }
+    cache[splits] = std::max(1, n);
+  }
+  return cache[splits];
+}
+
+int gemm_cluster_capacity(int M, int splits) {
+  switch (gemm_block_n(M)) {
+    case 32: return cluster_capacity_bn<32>(splits);
+    case 64: return cluster_capacity_bn<64>(splits);
+    case 128: return cluster_capacity_bn<128>(splits);
+    default: return cluster_capacity_bn<256>(splits);
+  }
+}
+
 int launch_gemm_cluster(const CUtensorMap* tm_w, const CUtensorMap* tm_x, void* y, int M, int N, int K, int splits,
                         unsigned* status, cudaStream_t stream, const PeerOut* peer) {
   if (K % 8 != 0 || N % 4 != 0 || splits < 1 || splits > 8) return -1;
@@ -786,16 +838,17 @@ int launch_gemm_persistent(const CUtensorMap* tm_w, const CUtensorMap* tm_x, voi
 }
 
 int launch_gemm_bf16(const CUtensorMap* tm_w, const CUtensorMap* tm_x, void* y, float* ws, int M, int N, int K,
-                     int splits, unsigned* status, cudaStream_t stream, int* counters, const PeerOut* peer) {
+                     int splits, unsigned* status, cudaStream_t stream, int* counters, const PeerOut* peer,
+                     int flags) {
   if (K % 8 != 0 || N % 4 != 0) return -1;
   if (splits > 1 && counters == nullptr && peer != nullptr && peer->world > 0) return -1;  // push needs the fused reduce
   const PeerOut none{};
   const PeerOut& pe = peer != nullptr ? *peer : none;
   switch (gemm_block_n(M)) {
-    case 32: return run_gemm<32>(*tm_w, *tm_x, y, ws, counters, M, N, K, splits, status, stream, pe);
-    case 64: return run_gemm<64>(*tm_w, *tm_x, y, ws, counters, M, N, K, splits, status, stream, pe);
-    case 128: return run_gemm<128>(*tm_w, *tm_x, y, ws, counters, M, N, K, splits, status, stream, pe);
-    default: return run_gemm<256>(*tm_w, *tm_x, y, ws, counters, M, N, K, splits, status, stream, pe);
+    case 32: return run_gemm<32>(*tm_w, *tm_x, y, ws, counters, M, N, K, splits, status, stream, pe, flags);
+    case 64: return run_gemm<64>(*tm_w, *tm_x, y, ws, counters, M, N, K, splits, status, stream, pe, flags);
+    case 128: return run_gemm<128>(*tm_w, *tm_x, y, ws, counters, M, N, K, splits, status, stream, pe, flags);
+    default: return run_gemm<256>(*tm_w, *tm_x, y, ws, counters, M, N, K, splits, status, stream, pe, flags);
   }
 }
 

@@ -53,10 +53,11 @@ int gemm_splits(int M, int N, int K, int num_sms);
 // reduced inside the GEMM by the last CTA of each tile; without, by a second kernel.
 int launch_gemm_bf16(const CUtensorMap* tm_w, const CUtensorMap* tm_x, void* y, float* ws, int M, int N, int K,
                      int splits, unsigned* status, cudaStream_t stream, int* counters = nullptr,
-                     const PeerOut* peer = nullptr);
+                     const PeerOut* peer = nullptr, int flags = 0);
 
 // Cluster split-K GEMM (partials reduced over DSMEM inside each tile's cluster; no workspace).
 int gemm_cluster_splits(int M, int N, int K, int num_sms);
+int gemm_cluster_capacity(int M, int splits);
 int launch_gemm_cluster(const CUtensorMap* tm_w, const CUtensorMap* tm_x, void* y, int M, int N, int K, int splits,
                         unsigned* status, cudaStream_t stream, const PeerOut* peer = nullptr);
 

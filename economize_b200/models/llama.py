@@ -140,13 +140,19 @@ class CausalLM(nn.Module):
         partial = False  # h is a row-parallel partial awaiting its all-reduce (tensor parallelism)
         for i in todo:
             layer = self.layers[i]
-            x, resid = self._norm(h, layer.attn_norm, resid, partial)
-            if i in capture:
-                aux[i] = resid
-            h = self._attention(layer, i, x, batch, cache, cos, sin)
-            x, resid = self._norm(h, layer.mlp_norm, resid, True)
-            h = self._mlp(layer, x, i)
-            partial = True
+            # a layer view may skip a sublayer (self-drafting): the pending branch output is added at the next norm
+            if not getattr(layer, "skip_attn", False):
+                x, resid = self._norm(h, layer.attn_norm, resid, partial)
+                if i in capture:
+                    aux[i] = resid
+                h = self._attention(layer, i, x, batch, cache, cos, sin)
+                partial = True
+            elif i in capture:
+                raise ValueError(f"cannot capture the input of layer {i}: its attention is skipped")
+            if not getattr(layer, "skip_mlp", False):
+                x, resid = self._norm(h, layer.mlp_norm, resid, partial)
+                h = self._mlp(layer, x, i)
+                partial = True
         out, resid = self._norm(h, self.norm, resid, partial)
         if c.num_layers in capture:
             aux[c.num_layers] = resid

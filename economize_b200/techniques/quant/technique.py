@@ -220,7 +220,7 @@ class DraftQuantTechnique(_QuantBase):
         """Quantization of the drafter happens when the drafting technique attaches (it attaches after weights)."""
 
     @torch.no_grad()
-    def quantize_drafter(self, technique: nn.Module) -> None:
+    def after_drafter(self, technique: nn.Module) -> None:
         cfg: DraftQuantConfig = self.config
         if not self.weights:
             for name, p in list(technique.named_parameters()):

@@ -174,3 +174,72 @@ class MedusaCE(Objective):
         loss = total / max(weight, 1e-9)
         metrics["loss"] = float(loss.detach())
         return loss, metrics
+
+
+def torch_block(layer, h: torch.Tensor, config, cos: torch.Tensor, sin: torch.Tensor) -> torch.Tensor:
+    """A pre-norm decoder block in plain PyTorch (autograd, causal attention over the whole row): the residual
+    stream ``h [B, S, H]`` in, the block's output stream out. Used to train technique-owned blocks."""
+    import torch.nn.functional as F
+
+    from ..ops.reference import rmsnorm
+
+    eps = config.rms_norm_eps
+    batch, length, _ = h.shape
+    heads, kv_heads, hd = config.num_heads, config.num_kv_heads, config.head_dim
+    x = rmsnorm(h, layer.attn_norm, eps)[0]
+    q, k, v = F.linear(x, layer.wqkv, layer.bqkv).split([heads * hd, kv_heads * hd, kv_heads * hd], -1)
+    q = q.reshape(batch, length, heads, hd)
+    k = k.reshape(batch, length, kv_heads, hd)
+    if layer.q_norm is not None:
+        q, k = rmsnorm(q, layer.q_norm, eps)[0], rmsnorm(k, layer.k_norm, eps)[0]
+    c, s = cos[:length][None, :, None].to(q.dtype), sin[:length][None, :, None].to(q.dtype)
+
+    def rot(t):
+        a, b = t[..., : hd // 2], t[..., hd // 2:]
+        return torch.cat([a * c - b * s, b * c + a * s], -1)
+
+    q, k = rot(q).transpose(1, 2), rot(k).transpose(1, 2)
+    v = v.reshape(batch, length, kv_heads, hd).transpose(1, 2)
+    group = heads // kv_heads
+    o = F.scaled_dot_product_attention(q, k.repeat_interleave(group, 1), v.repeat_interleave(group, 1),
+                                       is_causal=True)
+    h = h + F.linear(o.transpose(1, 2).reshape(batch, length, heads * hd), layer.wo)
+    x = rmsnorm(h, layer.mlp_norm, eps)[0]
+    g, u = F.linear(x, layer.w_gate_up).chunk(2, -1)
+    return h + F.linear(F.silu(g) * u, layer.w_down)
+
+
+@OBJECTIVES.register("kangaroo_distill")
+class KangarooDistill(Objective):
+    """Kangaroo's adapter training: the adapter blocks read the target's residual stream after ``exit_layer``
+    blocks and, through the target's final norm and LM head, learn the target's greedy next token (cross-entropy)."""
+
+    name = "kangaroo_distill"
+    defaults = OptimDefaults(lr=5e-4, warmup_steps=10)
+
+    def __init__(self, model) -> None:
+        super().__init__(model)
+        if "kangaroo" not in model.techniques:
+            raise ConfigError("kangaroo_distill needs an attached kangaroo technique")
+        self.tech = model.techniques["kangaroo"]
+
+    def parameters(self) -> list[torch.nn.Parameter]:
+        return [p for p in self.tech.adapter.parameters() if p.requires_grad]
+
+    def loss(self, tokens: torch.Tensor) -> tuple[torch.Tensor, dict[str, float]]:
+        import torch.nn.functional as F
+
+        from ..ops.reference import rmsnorm
+
+        target = self.model.model
+        k = self.tech.config.exit_layer
+        aux, labels = teacher_pass(self.model, tokens, (k,))
+        h = aux[k].detach()
+        cos, sin = target.rope_tables(tokens.shape[1])
+        for block in self.tech.adapter:
+            h = torch_block(block, h, target.config, cos, sin)
+        logits = F.linear(rmsnorm(h, target.norm, target.config.rms_norm_eps)[0], target.head_weight).float()
+        loss = F.cross_entropy(logits.reshape(-1, logits.shape[-1]), labels.reshape(-1))
+        with torch.no_grad():
+            acc = (logits.argmax(-1) == labels).float().mean()
+        return loss, {"loss": float(loss.detach()), "acc": float(acc)}
