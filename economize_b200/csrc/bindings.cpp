@@ -111,25 +111,38 @@ const CUtensorMap* tensor_map(const void* base, uint64_t rows, uint64_t cols, ui
   return tensor_map_ex(base, 2, rows, cols, stride * 2, 64, box, 128);
 }
 
+// A split-K partials input is an fp32 tensor with one extra leading dimension [splits, ...] (see linear_parts);
+// returns (splits, the bf16 shape it stands for).
+std::pair<int, std::vector<int64_t>> parts_of(const Tensor& x) {
+  if (x.scalar_type() == at::kBFloat16) return {0, x.sizes().vec()};
+  TORCH_CHECK(x.scalar_type() == at::kFloat && x.dim() >= 2 && x.is_contiguous(),
+              "expected a bf16 tensor or contiguous fp32 split-K partials [splits, ...]");
+  return {static_cast<int>(x.size(0)), std::vector<int64_t>(x.sizes().begin() + 1, x.sizes().end())};
+}
+
 std::tuple<Tensor, Tensor> rmsnorm(Tensor x, Tensor w, double eps, c10::optional<Tensor> resid) {
   CHECK_CUDA(x);
-  CHECK_BF16(x);
   CHECK_BF16(w);
   c10::cuda::CUDAGuard guard(x.device());
   x = x.contiguous();
-  const int hidden = static_cast<int>(x.size(-1));
-  const int rows = static_cast<int>(x.numel() / hidden);
+  const auto [splits, shape] = parts_of(x);
+  const int hidden = static_cast<int>(shape.back());
+  int64_t numel = 1;
+  for (auto d : shape) numel *= d;
+  const int rows = static_cast<int>(numel / hidden);
   Tensor r;
   if (resid.has_value()) {
     r = resid->contiguous();
     CHECK_BF16(r);
-    TORCH_CHECK(r.numel() == x.numel(), "residual shape mismatch");
+    TORCH_CHECK(r.numel() == numel, "residual shape mismatch");
   }
-  auto out = at::empty_like(x);
-  auto resid_out = at::empty_like(x);
-  const int rc = ecz::launch_rmsnorm(x.data_ptr(), resid.has_value() ? r.data_ptr() : nullptr, w.data_ptr(),
-                                     out.data_ptr(), resid_out.data_ptr(), rows, hidden, static_cast<float>(eps),
-                                     at::cuda::getCurrentCUDAStream());
+  const auto opts = x.options().dtype(at::kBFloat16);
+  auto out = at::empty(shape, opts);
+  auto resid_out = at::empty(shape, opts);
+  const int rc = ecz::launch_rmsnorm(splits ? nullptr : x.data_ptr(), resid.has_value() ? r.data_ptr() : nullptr,
+                                     w.data_ptr(), out.data_ptr(), resid_out.data_ptr(), rows, hidden,
+                                     static_cast<float>(eps), at::cuda::getCurrentCUDAStream(),
+                                     splits ? x.data_ptr<float>() : nullptr, splits);
   TORCH_CHECK(rc == 0, "rmsnorm: unsupported hidden size ", hidden);
   return {out, resid_out};
 }
@@ -152,29 +165,30 @@ Tensor rope_store(Tensor qkv, Tensor positions, Tensor cos, Tensor sin, int64_t 
                   c10::optional<Tensor> k_norm, double eps, int64_t q_offset, c10::optional<Tensor> k_scale,
                   c10::optional<Tensor> v_scale) {
   CHECK_CUDA(qkv);
-  CHECK_BF16(qkv);
   TORCH_CHECK(D == 128, "rope_store: head_dim must be 128, got ", D);
+  const auto [qkv_splits, qkv_shape] = parts_of(qkv);
   const bool fp8 = fp8_cache(k_cache, k_scale, v_scale, Hkv);
   TORCH_CHECK(v_cache.scalar_type() == k_cache.scalar_type(), "K and V caches must share a dtype");
   CHECK_I32(positions);
   CHECK_I32(kv_len);
   CHECK_I32(n_new);
   TORCH_CHECK(cos.scalar_type() == at::kFloat && sin.scalar_type() == at::kFloat, "rope tables must be fp32");
-  TORCH_CHECK(qkv.dim() == 3 && k_cache.dim() == 4, "rope_store expects qkv [B, T, W] and caches [B, Hkv, S, D]");
+  TORCH_CHECK(k_cache.dim() == 4, "rope_store expects caches [B, Hkv, S, D]");
   TORCH_CHECK(k_cache.is_contiguous() && v_cache.is_contiguous(), "caches must be contiguous");
   c10::cuda::CUDAGuard guard(qkv.device());
-  qkv = qkv.contiguous();
+  if (!qkv_splits) qkv = qkv.contiguous();
   positions = positions.contiguous();
-  const int B = static_cast<int>(qkv.size(0)), T = static_cast<int>(qkv.size(1));
-  TORCH_CHECK(qkv.size(2) == (H + 2 * Hkv) * D, "qkv width mismatch");
-  auto q = at::empty({B, T, H, D}, qkv.options());
+  const int B = static_cast<int>(qkv_shape[0]), T = static_cast<int>(qkv_shape[1]);
+  TORCH_CHECK(qkv_shape.size() == 3 && qkv_shape[2] == (H + 2 * Hkv) * D, "qkv width mismatch");
+  auto q = at::empty({B, T, H, D}, qkv.options().dtype(at::kBFloat16));
   const int rc = ecz::launch_rope_store(
-      qkv.data_ptr(), positions.data_ptr<int>(), cos.data_ptr<float>(), sin.data_ptr<float>(), q.data_ptr(),
+      qkv_splits ? nullptr : qkv.data_ptr(), positions.data_ptr<int>(), cos.data_ptr<float>(), sin.data_ptr<float>(), q.data_ptr(),
       k_cache.data_ptr(), v_cache.data_ptr(), kv_len.data_ptr<int>(), n_new.data_ptr<int>(),
       q_norm.has_value() ? q_norm->data_ptr() : nullptr, k_norm.has_value() ? k_norm->data_ptr() : nullptr,
       static_cast<float>(eps), B, T, static_cast<int>(H), static_cast<int>(Hkv), static_cast<int>(D),
       static_cast<int>(k_cache.size(2)), static_cast<int>(q_offset), at::cuda::getCurrentCUDAStream(),
-      fp8 ? k_scale->data_ptr<float>() : nullptr, fp8 ? v_scale->data_ptr<float>() : nullptr);
+      fp8 ? k_scale->data_ptr<float>() : nullptr, fp8 ? v_scale->data_ptr<float>() : nullptr,
+      qkv_splits ? qkv.data_ptr<float>() : nullptr, qkv_splits);
   TORCH_CHECK(rc == 0, "rope_store: unsupported head_dim ", D);
   return q;
 }
@@ -229,20 +243,23 @@ Tensor attention(Tensor q, Tensor k_cache, Tensor v_cache, Tensor kv_len, Tensor
 
 Tensor silu_mul(Tensor gu) {
   CHECK_CUDA(gu);
-  CHECK_BF16(gu);
   c10::cuda::CUDAGuard guard(gu.device());
   gu = gu.contiguous();
-  const int F2 = static_cast<int>(gu.size(-1));
-  const int rows = static_cast<int>(gu.numel() / F2);
-  std::vector<int64_t> shape(gu.sizes().begin(), gu.sizes().end());
+  auto [splits, shape] = parts_of(gu);
+  const int F2 = static_cast<int>(shape.back());
+  int64_t numel = 1;
+  for (auto d : shape) numel *= d;
+  const int rows = static_cast<int>(numel / F2);
   shape.back() = F2 / 2;
-  auto out = at::empty(shape, gu.options());
-  const int rc = ecz::launch_silu_mul(gu.data_ptr(), out.data_ptr(), rows, F2 / 2, at::cuda::getCurrentCUDAStream());
+  auto out = at::empty(shape, gu.options().dtype(at::kBFloat16));
+  const int rc = ecz::launch_silu_mul(splits ? nullptr : gu.data_ptr(), out.data_ptr(), rows, F2 / 2,
+                                      at::cuda::getCurrentCUDAStream(), splits ? gu.data_ptr<float>() : nullptr,
+                                      splits);
   TORCH_CHECK(rc == 0, "silu_mul: width must be a multiple of 16");
   return out;
 }
 
-Tensor linear(Tensor x, Tensor w) {
+Tensor linear_bf16(Tensor x, Tensor w) {
   CHECK_CUDA(x);
   CHECK_BF16(x);
   CHECK_BF16(w);
@@ -313,6 +330,35 @@ Tensor linear_wq(Tensor x, Tensor qweight, Tensor scales, c10::optional<Tensor> 
                                      status_word(x.device()), at::cuda::getCurrentCUDAStream());
   TORCH_CHECK(rc == 0, "linear_wq: launch failed (", rc, ")");
   return y;
+}
+
+// x @ w.T for a consumer that sums split-K partials itself (rmsnorm, silu_mul, rope_store): a bf16 [M, N] result
+// when the GEMM needs no split, else the fp32 partials [splits, M, N] of the non-cluster split-K kernel (two CTAs
+// per SM). Tiles wider than 64 tokens take the regular path.
+Tensor linear_parts(Tensor x, Tensor w) {
+  CHECK_CUDA(x);
+  CHECK_BF16(x);
+  CHECK_BF16(w);
+  TORCH_CHECK(x.dim() == 2 && w.dim() == 2 && x.size(1) == w.size(1), "linear_parts expects x [M, K] and w [N, K]");
+  const int M = static_cast<int>(x.size(0)), K = static_cast<int>(x.size(1)), N = static_cast<int>(w.size(0));
+  const int bn = ecz::gemm_block_n(M);
+  if (bn > 64 || M == 0) return linear_bf16(x, w);
+  c10::cuda::CUDAGuard guard(x.device());
+  x = x.contiguous();
+  w = w.contiguous();
+  const int sms = num_sms(x.get_device());
+  int splits = std::min(8, ecz::gemm_splits(M, N, K, 2 * sms));
+  const int total_kb = (K + 63) / 64, kbps = (total_kb + splits - 1) / splits;
+  splits = (total_kb + kbps - 1) / kbps;  // the launcher drops empty splits the same way
+  const CUtensorMap* tw = tensor_map(w.data_ptr(), N, K, K, 128);
+  const CUtensorMap* tx = tensor_map(x.data_ptr(), M, K, K, bn);
+  cudaStream_t stream = at::cuda::getCurrentCUDAStream();
+  Tensor out = splits > 1 ? at::empty({splits, M, N}, x.options().dtype(at::kFloat)) : at::empty({M, N}, x.options());
+  const int rc = ecz::launch_gemm_bf16(tw, tx, splits > 1 ? nullptr : out.data_ptr(),
+                                       splits > 1 ? out.data_ptr<float>() : nullptr, M, N, K, splits,
+                                       status_word(x.device()), stream, nullptr, nullptr, 3);
+  TORCH_CHECK(rc == 0, "linear_parts: launch failed (", rc, ")");
+  return out;
 }
 
 // Explicit GEMM variant (tuning and benchmarks): mode 1 cluster split-K (DSMEM reduction), 2 split-K through a
@@ -604,10 +650,11 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
         py::arg("scale"), py::arg("q_offset"), py::arg("trace") = py::none(), py::arg("k_scale") = py::none(),
         py::arg("v_scale") = py::none());
   m.def("silu_mul", &silu_mul, "SwiGLU activation of [gate; up]");
+  m.def("linear_parts", &linear_parts, "x @ w.T as bf16 or fp32 split-K partials for a fusing consumer");
   m.def("linear_variant", &linear_variant, "x @ w.T through an explicit GEMM variant (tuning)");
   m.def("gemm_cluster_capacity", &gemm_cluster_capacity, "resident clusters of the split-K cluster GEMM");
   m.def("raise_formatted", &raise_formatted, "raise a formatted RuntimeError (exception-path self test)");
-  m.def("linear", &linear, "x @ w.T on tcgen05 (swap-AB, split-K)");
+  m.def("linear", &linear_bf16, "x @ w.T on tcgen05 (swap-AB, split-K)");
   m.def("linear_wq", &linear_wq, "weight-only quantized x @ dequant(w).T (int4 / int8 / fp8 weights)", py::arg("x"),
         py::arg("qweight"), py::arg("scales"), py::arg("zeros"), py::arg("fmt"), py::arg("group"), py::arg("splits") = 0);
   m.def("argmax", &argmax, "row argmax");

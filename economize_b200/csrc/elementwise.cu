@@ -16,18 +16,52 @@
 
 namespace ecz {
 
+// Split-K partials: a GEMM may leave `splits` fp32 partial products [splits][elems] instead of its bf16 output; the
+// consuming kernel sums them in split order and rounds to bf16, which is exactly the value the GEMM's own reduction
+// would have stored. These load 8 (2) consecutive values of element offset `off` either way.
+struct Parts {
+  const float* p = nullptr;
+  int splits = 0;
+  long stride = 0;  // elements between consecutive partials
+};
+
+__device__ __forceinline__ uint4 load8(const bf16* x, const Parts& parts, size_t off) {
+  if (parts.p == nullptr) return *reinterpret_cast<const uint4*>(x + off);
+  float4 a = *reinterpret_cast<const float4*>(parts.p + off);
+  float4 b = *reinterpret_cast<const float4*>(parts.p + off + 4);
+  for (int s = 1; s < parts.splits; ++s) {
+    const float4 c = *reinterpret_cast<const float4*>(parts.p + s * parts.stride + off);
+    const float4 d = *reinterpret_cast<const float4*>(parts.p + s * parts.stride + off + 4);
+    a.x += c.x; a.y += c.y; a.z += c.z; a.w += c.w;
+    b.x += d.x; b.y += d.y; b.z += d.z; b.w += d.w;
+  }
+  __nv_bfloat162 h[4] = {__floats2bfloat162_rn(a.x, a.y), __floats2bfloat162_rn(a.z, a.w),
+                         __floats2bfloat162_rn(b.x, b.y), __floats2bfloat162_rn(b.z, b.w)};
+  return *reinterpret_cast<uint4*>(h);
+}
+
+__device__ __forceinline__ __nv_bfloat162 load2(const bf16* x, const Parts& parts, size_t off) {
+  if (parts.p == nullptr) return *reinterpret_cast<const __nv_bfloat162*>(x + off);
+  float2 a = *reinterpret_cast<const float2*>(parts.p + off);
+  for (int s = 1; s < parts.splits; ++s) {
+    const float2 c = *reinterpret_cast<const float2*>(parts.p + s * parts.stride + off);
+    a.x += c.x; a.y += c.y;
+  }
+  return __floats2bfloat162_rn(a.x, a.y);
+}
+
 // ---------------------------------------------------------------------------------------------------------------
 // RMSNorm
 // ---------------------------------------------------------------------------------------------------------------
 template <int kMaxVec>
 __global__ void __launch_bounds__(256) rmsnorm_kernel(const bf16* __restrict__ x, const bf16* __restrict__ resid,
                                                       const bf16* __restrict__ w, bf16* __restrict__ out,
-                                                      bf16* __restrict__ resid_out, int hidden, float eps) {
+                                                      bf16* __restrict__ resid_out, int hidden, float eps,
+                                                      Parts parts) {
   pdl_trigger();
   pdl_wait();
   const int row = blockIdx.x;
   const int nvec = hidden / 8;
-  const uint4* xv = reinterpret_cast<const uint4*>(x + static_cast<size_t>(row) * hidden);
   const uint4* rv = resid ? reinterpret_cast<const uint4*>(resid + static_cast<size_t>(row) * hidden) : nullptr;
   uint4* ro = reinterpret_cast<uint4*>(resid_out + static_cast<size_t>(row) * hidden);
   float vals[kMaxVec][8];
@@ -36,7 +70,7 @@ __global__ void __launch_bounds__(256) rmsnorm_kernel(const bf16* __restrict__ x
   for (int i = 0; i < kMaxVec; ++i) {
     const int v = threadIdx.x + i * blockDim.x;
     if (v < nvec) {
-      uint4 a = xv[v];
+      uint4 a = load8(x, parts, static_cast<size_t>(row) * hidden + v * 8);
       const bf16* ap = reinterpret_cast<const bf16*>(&a);
       uint4 s;
       bf16* sp = reinterpret_cast<bf16*>(&s);
@@ -86,7 +120,8 @@ __global__ void __launch_bounds__(256) rmsnorm_kernel(const bf16* __restrict__ x
 }
 
 int launch_rmsnorm(const void* x, const void* resid, const void* w, void* out, void* resid_out, int rows, int hidden,
-                   float eps, cudaStream_t stream) {
+                   float eps, cudaStream_t stream, const float* x_parts, int splits) {
+  const Parts parts{x_parts, splits, static_cast<long>(rows) * hidden};
   if (hidden % 8 != 0 || hidden > 256 * 8 * 8) return -1;
   const int nvec = hidden / 8;
   int threads = nvec < 256 ? ((nvec + 31) / 32) * 32 : 256;
@@ -94,7 +129,7 @@ int launch_rmsnorm(const void* x, const void* resid, const void* w, void* out, v
   auto args = [&](auto kernel) {
     launch_pdl(kernel, dim3(rows), dim3(threads), 0, stream, static_cast<const bf16*>(x),
                static_cast<const bf16*>(resid), static_cast<const bf16*>(w), static_cast<bf16*>(out),
-               static_cast<bf16*>(resid_out), hidden, eps);
+               static_cast<bf16*>(resid_out), hidden, eps, parts);
   };
   if (per <= 1) args(rmsnorm_kernel<1>);
   else if (per <= 2) args(rmsnorm_kernel<2>);
@@ -114,7 +149,7 @@ __global__ void __launch_bounds__(256) rope_store_kernel(
     const float* __restrict__ sin_t, bf16* __restrict__ q_out, bf16* __restrict__ k_cache,
     bf16* __restrict__ v_cache, const int* __restrict__ kv_len, const int* __restrict__ n_new,
     const bf16* __restrict__ q_norm, const bf16* __restrict__ k_norm, float eps, int tokens, int T, int H, int Hkv,
-    int S, int q_offset, const float* __restrict__ k_scale, const float* __restrict__ v_scale) {
+    int S, int q_offset, const float* __restrict__ k_scale, const float* __restrict__ v_scale, Parts parts) {
   pdl_trigger();
   pdl_wait();
   constexpr int D = 128;
@@ -127,11 +162,11 @@ __global__ void __launch_bounds__(256) rope_store_kernel(
   const int b = token / T, t = token % T;
   const bool is_q = head < H;
   const int width = (H + 2 * Hkv) * D;
-  const bf16* src = qkv + static_cast<size_t>(token) * width + (is_q ? head * D : H * D + (head - H) * D);
+  const size_t src = static_cast<size_t>(token) * width + (is_q ? head * D : H * D + (head - H) * D);
   // lane owns elements (2*lane, 2*lane+1) of the first half and their partners in the second half
   const int i0 = 2 * lane;
-  __nv_bfloat162 lo = *reinterpret_cast<const __nv_bfloat162*>(src + i0);
-  __nv_bfloat162 hi = *reinterpret_cast<const __nv_bfloat162*>(src + i0 + D / 2);
+  __nv_bfloat162 lo = load2(qkv, parts, src + i0);
+  __nv_bfloat162 hi = load2(qkv, parts, src + i0 + D / 2);
   float x0 = __bfloat162float(lo.x), x1 = __bfloat162float(lo.y);
   float y0 = __bfloat162float(hi.x), y1 = __bfloat162float(hi.y);
   const bf16* nw = is_q ? q_norm : k_norm;
@@ -166,7 +201,7 @@ __global__ void __launch_bounds__(256) rope_store_kernel(
   const size_t off = ((static_cast<size_t>(b) * Hkv + kvh) * S + slot) * D;
   if (k_scale != nullptr) {
     // fp8 cache: e4m3 codes of value / scale (quotient rounded to fp32 first, then to e4m3 with saturation)
-    const bf16* vsrc = qkv + static_cast<size_t>(token) * width + (H + Hkv) * D + kvh * D;
+    const size_t vsrc = static_cast<size_t>(token) * width + (H + Hkv) * D + kvh * D;
     const float sk = k_scale[kvh], sv = v_scale[kvh];
     uint8_t* kc = reinterpret_cast<uint8_t*>(k_cache) + off;
     uint8_t* vc = reinterpret_cast<uint8_t*>(v_cache) + off;
@@ -176,31 +211,32 @@ __global__ void __launch_bounds__(256) rope_store_kernel(
     };
     put(kc + i0, __fdiv_rn(bf16r(r0), sk), __fdiv_rn(bf16r(r1), sk));
     put(kc + i0 + D / 2, __fdiv_rn(bf16r(r2), sk), __fdiv_rn(bf16r(r3), sk));
-    const __nv_bfloat162 va = *reinterpret_cast<const __nv_bfloat162*>(vsrc + i0);
-    const __nv_bfloat162 vb = *reinterpret_cast<const __nv_bfloat162*>(vsrc + i0 + D / 2);
+    const __nv_bfloat162 va = load2(qkv, parts, vsrc + i0);
+    const __nv_bfloat162 vb = load2(qkv, parts, vsrc + i0 + D / 2);
     put(vc + i0, __fdiv_rn(__bfloat162float(va.x), sv), __fdiv_rn(__bfloat162float(va.y), sv));
     put(vc + i0 + D / 2, __fdiv_rn(__bfloat162float(vb.x), sv), __fdiv_rn(__bfloat162float(vb.y), sv));
     return;
   }
   *reinterpret_cast<__nv_bfloat162*>(k_cache + off + i0) = __floats2bfloat162_rn(r0, r1);
   *reinterpret_cast<__nv_bfloat162*>(k_cache + off + i0 + D / 2) = __floats2bfloat162_rn(r2, r3);
-  const bf16* vsrc = qkv + static_cast<size_t>(token) * width + (H + Hkv) * D + kvh * D;
-  *reinterpret_cast<__nv_bfloat162*>(v_cache + off + i0) = *reinterpret_cast<const __nv_bfloat162*>(vsrc + i0);
-  *reinterpret_cast<__nv_bfloat162*>(v_cache + off + i0 + D / 2) =
-      *reinterpret_cast<const __nv_bfloat162*>(vsrc + i0 + D / 2);
+  const size_t vsrc = static_cast<size_t>(token) * width + (H + Hkv) * D + kvh * D;
+  *reinterpret_cast<__nv_bfloat162*>(v_cache + off + i0) = load2(qkv, parts, vsrc + i0);
+  *reinterpret_cast<__nv_bfloat162*>(v_cache + off + i0 + D / 2) = load2(qkv, parts, vsrc + i0 + D / 2);
 }
 
 int launch_rope_store(const void* qkv, const int* positions, const float* cos_t, const float* sin_t, void* q_out,
                       void* k_cache, void* v_cache, const int* kv_len, const int* n_new, const void* q_norm,
                       const void* k_norm, float eps, int B, int T, int H, int Hkv, int D, int S, int q_offset,
-                      cudaStream_t stream, const float* k_scale, const float* v_scale) {
+                      cudaStream_t stream, const float* k_scale, const float* v_scale, const float* qkv_parts,
+                      int splits) {
   if (D != 128) return -1;
+  const Parts parts{qkv_parts, splits, static_cast<long>(B) * T * (H + 2 * Hkv) * D};
   const long warps = static_cast<long>(B) * T * (H + Hkv);
   const int blocks = static_cast<int>((warps * 32 + 255) / 256);
   launch_pdl(rope_store_kernel, dim3(blocks), dim3(256), 0, stream, static_cast<const bf16*>(qkv), positions, cos_t,
              sin_t, static_cast<bf16*>(q_out), static_cast<bf16*>(k_cache), static_cast<bf16*>(v_cache), kv_len,
              n_new, static_cast<const bf16*>(q_norm), static_cast<const bf16*>(k_norm), eps, B * T, T, H, Hkv, S,
-             q_offset, k_scale, v_scale);
+             q_offset, k_scale, v_scale, parts);
   return 0;
 }
 
@@ -208,15 +244,15 @@ int launch_rope_store(const void* qkv, const int* positions, const float* cos_t,
 // SiLU(gate) * up
 // ---------------------------------------------------------------------------------------------------------------
 __global__ void __launch_bounds__(256) silu_mul_kernel(const bf16* __restrict__ gu, bf16* __restrict__ out,
-                                                       int rows, int F) {
+                                                       int rows, int F, Parts parts) {
   pdl_trigger();
   pdl_wait();
   const long total = static_cast<long>(rows) * (F / 8);
   for (long i = blockIdx.x * static_cast<long>(blockDim.x) + threadIdx.x; i < total;
        i += static_cast<long>(gridDim.x) * blockDim.x) {
     const long r = i / (F / 8), c = i % (F / 8);
-    const uint4 g = reinterpret_cast<const uint4*>(gu + r * 2 * F)[c];
-    const uint4 u = reinterpret_cast<const uint4*>(gu + r * 2 * F + F)[c];
+    const uint4 g = load8(gu, parts, static_cast<size_t>(r) * 2 * F + c * 8);
+    const uint4 u = load8(gu, parts, static_cast<size_t>(r) * 2 * F + F + c * 8);
     const bf16* gp = reinterpret_cast<const bf16*>(&g);
     const bf16* up = reinterpret_cast<const bf16*>(&u);
     uint4 o;
@@ -231,13 +267,15 @@ __global__ void __launch_bounds__(256) silu_mul_kernel(const bf16* __restrict__ 
   }
 }
 
-int launch_silu_mul(const void* gu, void* out, int rows, int F, cudaStream_t stream) {
+int launch_silu_mul(const void* gu, void* out, int rows, int F, cudaStream_t stream, const float* gu_parts,
+                    int splits) {
   if (F % 8 != 0) return -1;
+  const Parts parts{gu_parts, splits, static_cast<long>(rows) * 2 * F};
   const long total = static_cast<long>(rows) * (F / 8);
   int blocks = static_cast<int>(std::min<long>((total + 255) / 256, 148L * 16));
   if (blocks < 1) blocks = 1;
   launch_pdl(silu_mul_kernel, dim3(blocks), dim3(256), 0, stream, static_cast<const bf16*>(gu),
-             static_cast<bf16*>(out), rows, F);
+             static_cast<bf16*>(out), rows, F, parts);
   return 0;
 }
 

@@ -30,13 +30,17 @@ struct AttnPlan {
 };
 
 // elementwise.cu
+// x_parts / qkv_parts / gu_parts: optional fp32 split-K partials [splits][...] of the input, summed in split order
+// and rounded to bf16 in place of reading the bf16 input.
 int launch_rmsnorm(const void* x, const void* resid, const void* w, void* out, void* resid_out, int rows, int hidden,
-                   float eps, cudaStream_t stream);
+                   float eps, cudaStream_t stream, const float* x_parts = nullptr, int splits = 0);
 int launch_rope_store(const void* qkv, const int* positions, const float* cos_t, const float* sin_t, void* q_out,
                       void* k_cache, void* v_cache, const int* kv_len, const int* n_new, const void* q_norm,
                       const void* k_norm, float eps, int B, int T, int H, int Hkv, int D, int S, int q_offset,
-                      cudaStream_t stream, const float* k_scale = nullptr, const float* v_scale = nullptr);
-int launch_silu_mul(const void* gu, void* out, int rows, int F, cudaStream_t stream);
+                      cudaStream_t stream, const float* k_scale = nullptr, const float* v_scale = nullptr,
+                      const float* qkv_parts = nullptr, int splits = 0);
+int launch_silu_mul(const void* gu, void* out, int rows, int F, cudaStream_t stream, const float* gu_parts = nullptr,
+                    int splits = 0);
 int argmax_slices(int rows, int V);
 int launch_argmax(const void* x, bool is_bf16, int64_t* out, float* part_v, int* part_i, int rows, int V,
                   cudaStream_t stream);

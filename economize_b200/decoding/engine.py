@@ -268,7 +268,9 @@ class SpecEngine:
 
     # ---- cycles ------------------------------------------------------------------------------------------------
     def _run_cycles(self, st: _State, max_new: int, stop_tokens: list[int] | None) -> None:
-        use_graph = self.config.cuda_graphs and self.model.device.type == "cuda"
+        # drafters that search host-side structures (retrieval, suffix trees) synchronise with the host every cycle
+        use_graph = self.config.cuda_graphs and self.model.device.type == "cuda" and \
+            getattr(self.drafter, "graph_safe", True)
         key = (st.batch, st.capacity, st.out_cap)
         remaining = max_new - 1  # the prefill produced the first token
         per_cycle = self.tokens_per_cycle

@@ -179,7 +179,7 @@ class CausalLM(nn.Module):
         c = self.config
         if self.observer is not None:
             self.observer(index, "wqkv", x)
-        qkv = ops.linear(x, layer.wqkv, layer.bqkv)
+        qkv = self._linear(x, layer.wqkv) if layer.bqkv is None else ops.linear(x, layer.wqkv, layer.bqkv)
         k_cache, v_cache = cache.layer(index)
         k_scale, v_scale = cache.layer_scales(index)
         q = ops.rope_store(qkv, batch.positions, cos, sin, self.local["num_heads"], self.local["num_kv_heads"],
@@ -193,6 +193,14 @@ class CausalLM(nn.Module):
             self.observer(index, "wo", o)
         return self._row_linear(o, layer.wo)
 
+    def _linear(self, x: torch.Tensor, weight):
+        """A projection whose consumer is one of the engine's fused elementwise kernels: without tensor
+        parallelism the GEMM may hand over its split-K partials (:class:`~economize_b200.ops.Partials`), which the
+        consumer reduces while reading them."""
+        if self.tp is None or self.tp.size == 1:
+            return ops.linear_parts(x, weight)
+        return ops.linear(x, weight)
+
     def _row_linear(self, x: torch.Tensor, weight: torch.Tensor):
         """A row-parallel projection (``wo``, ``w_down``): under fused tensor parallelism the GEMM pushes its
         partial output to the peers itself and returns a :class:`~economize_b200.parallel.comm.Pushed` marker."""
@@ -200,7 +208,7 @@ class CausalLM(nn.Module):
         if tp is not None and tp.size > 1 and tp.fused and tp.comm is not None and isinstance(weight, torch.Tensor) \
                 and tp.comm.fits(x.numel() // x.shape[-1]):
             return tp.comm.gemm_push(x, weight)
-        return ops.linear(x, weight)
+        return self._linear(x, weight)
 
     def _mlp(self, layer: DecoderLayer, x: torch.Tensor, index: int = -1) -> torch.Tensor:
         if layer.router is not None:
@@ -209,7 +217,7 @@ class CausalLM(nn.Module):
             return moe_mlp(x, layer.router, layer.w_gate_up, layer.w_down, self.config.experts_per_token)
         if self.observer is not None:
             self.observer(index, "w_gate_up", x)
-        a = ops.silu_mul(ops.linear(x, layer.w_gate_up))
+        a = ops.silu_mul(self._linear(x, layer.w_gate_up))
         if self.observer is not None:
             self.observer(index, "w_down", a)
         return self._row_linear(a, layer.w_down)

@@ -20,6 +20,8 @@ __all__ = [
     "greedy_accept",
     "kv_compact",
     "linear",
+    "linear_parts",
+    "Partials",
     "load_error",
     "require",
     "rmsnorm",
@@ -32,11 +34,55 @@ __all__ = [
 ]
 
 
-def rmsnorm(x: torch.Tensor, weight: torch.Tensor, eps: float,
+class Partials:
+    """Split-K partial products ``data [splits, ..., N]`` (fp32) of a projection whose consumer sums them (in split
+    order, rounded to bf16: the value the GEMM would have stored) instead of the GEMM reducing them itself."""
+
+    __slots__ = ("data",)
+
+    def __init__(self, data: torch.Tensor) -> None:
+        self.data = data
+
+    @property
+    def shape(self) -> torch.Size:
+        return self.data.shape[1:]
+
+    @property
+    def is_cuda(self) -> bool:
+        return True
+
+    def numel(self) -> int:
+        return self.data[0].numel()
+
+    def sum(self) -> torch.Tensor:
+        """The bf16 tensor the partials stand for."""
+        acc = self.data[0].clone()
+        for i in range(1, self.data.shape[0]):
+            acc += self.data[i]
+        return acc.to(torch.bfloat16)
+
+
+def _raw(x):
+    return x.data if isinstance(x, Partials) else x
+
+
+def linear_parts(x: torch.Tensor, weight) -> torch.Tensor | Partials:
+    """``x @ weight.T`` for a consumer that fuses the split-K reduction (:func:`rmsnorm`, :func:`silu_mul`,
+    :func:`rope_store`): :class:`Partials` on CUDA when the GEMM splits K, else the plain result."""
+    if not x.is_cuda or isinstance(weight, QWeight) or x.dtype != torch.bfloat16:
+        return linear(x, weight)
+    shape = x.shape
+    y = require().linear_parts(x.reshape(-1, shape[-1]), weight)
+    if y.dtype == torch.bfloat16:
+        return y.reshape(*shape[:-1], weight.shape[0])
+    return Partials(y.reshape(y.shape[0], *shape[:-1], weight.shape[0]))
+
+
+def rmsnorm(x: torch.Tensor | Partials, weight: torch.Tensor, eps: float,
             residual: torch.Tensor | None = None) -> tuple[torch.Tensor, torch.Tensor]:
     """Fused residual add + RMSNorm: ``(norm(x + residual) * weight, x + residual)`` over the last dim."""
     if x.is_cuda:
-        return require().rmsnorm(x, weight, float(eps), residual)
+        return require().rmsnorm(_raw(x), weight, float(eps), residual)
     return reference.rmsnorm(x, weight, eps, residual)
 
 
@@ -48,7 +94,7 @@ def rope_store(qkv: torch.Tensor, positions: torch.Tensor, cos: torch.Tensor, si
     """Fused (per-head RMSNorm +) rotary embedding of queries and keys and the KV-cache write (see
     :func:`.reference.rope_store`); fp8 caches are written as e4m3 codes of ``value / scale``."""
     if qkv.is_cuda:
-        return require().rope_store(qkv, positions, cos, sin, num_heads, num_kv_heads, head_dim, k_cache, v_cache,
+        return require().rope_store(_raw(qkv), positions, cos, sin, num_heads, num_kv_heads, head_dim, k_cache, v_cache,
                                     kv_len, n_new, q_norm, k_norm, float(eps), int(q_offset), k_scale, v_scale)
     return reference.rope_store(qkv, positions, cos, sin, num_heads, num_kv_heads, head_dim, k_cache, v_cache,
                                 kv_len, n_new, q_norm, k_norm, eps, q_offset, k_scale, v_scale)
@@ -68,9 +114,9 @@ def attention(q: torch.Tensor, k_cache: torch.Tensor, v_cache: torch.Tensor, kv_
                                v_scale=v_scale)
 
 
-def silu_mul(gate_up: torch.Tensor) -> torch.Tensor:
+def silu_mul(gate_up: torch.Tensor | Partials) -> torch.Tensor:
     if gate_up.is_cuda:
-        return require().silu_mul(gate_up)
+        return require().silu_mul(_raw(gate_up))
     return reference.silu_mul(gate_up)
 
 

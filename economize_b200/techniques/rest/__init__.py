@@ -1,0 +1,68 @@
+"""Retrieval-based speculative decoding (``rest``; He et al., 2024; economize ``techniques/rest`` and the shared
+``techniques/retrieval`` datastore): draft trees are the most frequent continuations, in a token datastore, of the
+longest suffix of the context found there. The datastore is built from ``corpus`` sequences (or calibration
+tokens) once; generation does not modify it."""
+
+from __future__ import annotations
+
+from dataclasses import dataclass
+from typing import Any, ClassVar
+
+import torch
+
+from ...core.technique import TechniqueConfig, register_technique
+from ...decoding.ngram_index import NGramIndex
+from ...errors import ConfigError
+from ...validation import check_positive
+from .._retrieval import RetrievalTechnique
+
+__all__ = ["RestConfig", "RestTechnique"]
+
+
+@dataclass(frozen=True)
+class RestConfig(TechniqueConfig):
+    technique: ClassVar[str] = "rest"
+    max_context: int = 16
+    max_depth: int = 6
+    budget: int = 32
+    branch: int = 4
+    min_match: int = 2
+    corpus: Any = None
+
+    def __post_init__(self) -> None:
+        for name in ("max_context", "max_depth", "budget", "branch", "min_match"):
+            check_positive(name, getattr(self, name))
+
+    def to_dict(self) -> dict[str, Any]:
+        out = super().to_dict()
+        out["corpus"] = None  # the datastore is rebuilt from the corpus, not serialised in the config
+        return out
+
+
+@register_technique
+class RestTechnique(RetrievalTechnique):
+    config_class = RestConfig
+    uses_local = False
+
+    def __init__(self, config: RestConfig, model) -> None:
+        super().__init__(config, model)
+        self.datastore = NGramIndex(config.max_context)
+        if config.corpus is not None:
+            self._build(config.corpus)
+
+    def _build(self, corpus) -> None:
+        seqs = corpus if not isinstance(corpus, torch.Tensor) else list(corpus.reshape(-1, corpus.shape[-1]))
+        self.datastore.extend([list(map(int, s)) for s in seqs])
+
+    def calibrate(self, calibration) -> None:
+        if self.datastore.size == 0:
+            self._build(calibration if not isinstance(calibration, torch.Tensor) else
+                        calibration.reshape(-1, calibration.shape[-1]))
+
+    def attach(self) -> None:
+        if self.datastore.size == 0:
+            raise ConfigError("rest needs a datastore: pass corpus= or calibration tokens")
+
+    def tree_for(self, row, local):
+        c = self.config
+        return self.datastore.draft_tree(row, c.budget, c.max_depth, c.branch, c.min_match)

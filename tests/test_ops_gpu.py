@@ -211,3 +211,52 @@ def test_rejection_kernel_matches_reference(cuda):
         j = int(n_ref[b])
         assert torch.equal(out_got[b, :j].cpu(), out_ref[b, :j])
         assert abs(int(out_got[b, j]) - int(out_ref[b, j])) <= 1 or out_got[b, j] == out_ref[b, j]
+
+
+@pytest.mark.parametrize("M,N,K", [(1, 6144, 4096), (61, 4096, 4096), (61, 1024, 14336), (40, 28672, 4096),
+                                   (7, 264, 512)])
+def test_linear_parts_matches_fp32(cuda, M, N, K):
+    g = torch.Generator(device=cuda).manual_seed(0)
+    x = torch.randn(M, K, device=cuda, generator=g).bfloat16()
+    w = (torch.randn(N, K, device=cuda, generator=g) * 0.02).bfloat16()
+    y = ops.linear_parts(x, w)
+    dense = y.sum() if isinstance(y, ops.Partials) else y
+    _close(dense, x.float() @ w.float().t(), 2e-2)
+
+
+def test_consumers_reduce_partials_exactly(cuda):
+    g = torch.Generator(device=cuda).manual_seed(1)
+    B, T, H, Hkv, D, S, hidden = 1, 61, 8, 2, 128, 256, 4096
+    x = torch.randn(B * T, hidden, device=cuda, generator=g).bfloat16()
+    # rmsnorm of a projection output
+    w = (torch.randn(hidden, hidden, device=cuda, generator=g) * 0.02).bfloat16()
+    p = ops.linear_parts(x, w)
+    assert isinstance(p, ops.Partials) and p.data.shape[0] > 1
+    nw = (1 + 0.1 * torch.randn(hidden, device=cuda, generator=g)).bfloat16()
+    r = torch.randn(B * T, hidden, device=cuda, generator=g).bfloat16()
+    a, ra = ops.rmsnorm(p, nw, 1e-5, r)
+    b, rb = ops.rmsnorm(p.sum(), nw, 1e-5, r)
+    assert torch.equal(a, b) and torch.equal(ra, rb)
+    # silu_mul of a gate/up projection
+    wgu = (torch.randn(2 * 1024, hidden, device=cuda, generator=g) * 0.02).bfloat16()
+    pg = ops.linear_parts(x, wgu)
+    assert torch.equal(ops.silu_mul(pg), ops.silu_mul(pg.sum()))
+    # rope_store of a qkv projection
+    wqkv = (torch.randn((H + 2 * Hkv) * D, hidden, device=cuda, generator=g) * 0.02).bfloat16()
+    pq = ops.linear_parts(x, wqkv)
+    pq = ops.Partials(pq.data.reshape(pq.data.shape[0], B, T, -1)) if isinstance(pq, ops.Partials) else pq
+    dense = pq.sum() if isinstance(pq, ops.Partials) else pq
+    inv = 1.0 / (10000 ** (torch.arange(0, D, 2, device=cuda).float() / D))
+    ang = torch.arange(512, device=cuda).float()[:, None] * inv[None]
+    cos, sin = ang.cos().contiguous(), ang.sin().contiguous()
+    pos = torch.arange(T, device=cuda, dtype=torch.int32)[None].contiguous()
+    kv_len = torch.zeros(B, dtype=torch.int32, device=cuda)
+    n_new = torch.full((B,), T, dtype=torch.int32, device=cuda)
+    outs = []
+    for qkv in (pq, dense):
+        kc = torch.zeros(B, Hkv, S, D, dtype=torch.bfloat16, device=cuda)
+        vc = torch.zeros_like(kc)
+        q = ops.rope_store(qkv, pos, cos, sin, H, Hkv, D, kc, vc, kv_len, n_new)
+        outs.append((q, kc, vc))
+    for u, v in zip(*outs):
+        assert torch.equal(u, v)
