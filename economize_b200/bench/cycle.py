@@ -1,0 +1,72 @@
+"""Decode-cycle benchmark: ``python -m economize_b200.bench.cycle [--tree/--chain/--plain] [--batch B]``.
+
+Builds the random-init Llama-3.1-8B architecture and an (untrained, early-exit-initialised) EAGLE-3 head, then
+times whole ``generate`` calls (CUDA events) for the chosen drafting mode and reports milliseconds per cycle and
+per generated token. The drafter is untrained, so the accepted length is close to one token per cycle; the number
+to read is the cycle time, which bounds tokens per second for any acceptance rate. ``--cycles-only`` stops after
+the warm-up generation (the case a launch-list capture profiles).
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+
+import torch
+
+__all__ = ["main"]
+
+
+def main(argv: list[str] | None = None) -> None:
+    import economize_b200 as eco
+    from economize_b200.models.config import llama31_8b
+    from economize_b200.models.llama import CausalLM, init_weights
+    from economize_b200.techniques.eagle3 import Eagle3Config
+
+    p = argparse.ArgumentParser(description=__doc__.splitlines()[0])
+    p.add_argument("--mode", choices=["tree", "chain", "plain"], default="tree")
+    p.add_argument("--batch", type=int, default=1)
+    p.add_argument("--prompt-len", type=int, default=512)
+    p.add_argument("--new-tokens", type=int, default=64)
+    p.add_argument("--iters", type=int, default=3)
+    p.add_argument("--layers", type=int, default=32)
+    p.add_argument("--cycles-only", action="store_true")
+    a = p.parse_args(argv)
+    cfg = llama31_8b()
+    cfg.num_layers = a.layers
+    target = init_weights(CausalLM(cfg, torch.bfloat16, "cuda"), seed=0)
+    eff = eco.apply(target, Eagle3Config(draft_vocab=32000))
+    eff.techniques["eagle3"].reset_parameters(seed=0, identity=True)
+    if a.mode == "tree":
+        dc = eco.DecodeConfig(cycle_length=7, draft_policy="dynamic_tree", cuda_graphs=True,
+                              draft_policy_options={"depth": 6, "topk": 10, "total_tokens": 60})
+    elif a.mode == "chain":
+        dc = eco.DecodeConfig(cycle_length=7, cuda_graphs=True)
+    else:
+        dc = eco.DecodeConfig(cycle_length=1, cuda_graphs=True)
+    g = torch.Generator().manual_seed(0)
+    prompts = [torch.randint(0, cfg.vocab_size, (a.prompt_len,), generator=g).cuda() for _ in range(a.batch)]
+    res = eff.decode_batch(prompts, a.new_tokens, decoding=dc)  # warm-up: graphs captured here
+    torch.cuda.synchronize()
+    if a.cycles_only:
+        return
+    times, cycles = [], 0
+    for _ in range(a.iters):
+        s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        s.record()
+        res = eff.decode_batch(prompts, a.new_tokens, decoding=dc)
+        e.record()
+        torch.cuda.synchronize()
+        times.append(s.elapsed_time(e))
+    cycles = max(int(r.cycles) for r in res)
+    ms = min(times)
+    tokens = sum(int(r.tokens.numel()) for r in res)
+    print(json.dumps({"mode": a.mode, "batch": a.batch, "prompt_len": a.prompt_len, "new_tokens": a.new_tokens,
+                      "layers": a.layers, "ms_per_generate": round(ms, 2), "cycles": cycles,
+                      "ms_per_cycle_incl_prefill": round(ms / max(cycles, 1), 3),
+                      "tokens_per_s": round(tokens / ms * 1e3, 1),
+                      "mean_accepted": round(sum(r.mean_accepted for r in res) / len(res), 3)}))
+
+
+if __name__ == "__main__":
+    main()

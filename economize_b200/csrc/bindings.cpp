@@ -361,6 +361,71 @@ Tensor linear_parts(Tensor x, Tensor w) {
   return out;
 }
 
+// Top-k routing of router logits [T, E] (bf16): expert ids [T, k] and renormalised weights [T, k] (fp32), each
+// pair's row in expert order pos [T, k] and the expert offsets [E + 1] (int32).
+std::tuple<Tensor, Tensor, Tensor, Tensor> moe_route(Tensor logits, int64_t k) {
+  CHECK_CUDA(logits);
+  CHECK_BF16(logits);
+  c10::cuda::CUDAGuard guard(logits.device());
+  logits = logits.contiguous();
+  const int T = static_cast<int>(logits.size(0)), E = static_cast<int>(logits.size(1));
+  auto i32 = logits.options().dtype(at::kInt);
+  auto ids = at::empty({T, k}, i32), pos = at::empty({T, k}, i32), offsets = at::empty({E + 1}, i32);
+  auto w = at::empty({T, k}, logits.options().dtype(at::kFloat));
+  const int rc = ecz::launch_moe_route(logits.data_ptr(), T, E, static_cast<int>(k), ids.data_ptr<int>(),
+                                       w.data_ptr<float>(), pos.data_ptr<int>(), offsets.data_ptr<int>(),
+                                       at::cuda::getCurrentCUDAStream());
+  TORCH_CHECK(rc == 0, "moe_route: at most 64 experts and top-8");
+  return {ids, w, pos, offsets};
+}
+
+Tensor moe_gather(Tensor x, Tensor pos) {
+  CHECK_CUDA(x);
+  CHECK_BF16(x);
+  CHECK_I32(pos);
+  c10::cuda::CUDAGuard guard(x.device());
+  x = x.contiguous();
+  const int T = static_cast<int>(pos.size(0)), k = static_cast<int>(pos.size(1)), H = static_cast<int>(x.size(1));
+  auto xs = at::empty({T * k, H}, x.options());
+  TORCH_CHECK(ecz::launch_moe_gather(x.data_ptr(), pos.data_ptr<int>(), xs.data_ptr(), T, k, H,
+                                     at::cuda::getCurrentCUDAStream()) == 0, "moe_gather: H % 8 != 0");
+  return xs;
+}
+
+Tensor moe_combine(Tensor y, Tensor pos, Tensor w) {
+  CHECK_CUDA(y);
+  CHECK_BF16(y);
+  c10::cuda::CUDAGuard guard(y.device());
+  const int T = static_cast<int>(pos.size(0)), k = static_cast<int>(pos.size(1)), H = static_cast<int>(y.size(1));
+  auto out = at::empty({T, H}, y.options());
+  TORCH_CHECK(ecz::launch_moe_combine(y.contiguous().data_ptr(), pos.data_ptr<int>(), w.data_ptr<float>(),
+                                      out.data_ptr(), T, k, H, at::cuda::getCurrentCUDAStream()) == 0,
+              "moe_combine failed");
+  return out;
+}
+
+// Grouped expert GEMM: rows offsets[e] .. offsets[e + 1] of xs [R, K] times expert e of w [E, N, K].
+Tensor linear_grouped(Tensor xs, Tensor w, Tensor offsets) {
+  CHECK_CUDA(xs);
+  CHECK_BF16(xs);
+  CHECK_BF16(w);
+  CHECK_I32(offsets);
+  TORCH_CHECK(w.dim() == 3 && xs.dim() == 2 && xs.size(1) == w.size(2), "linear_grouped: xs [R, K], w [E, N, K]");
+  c10::cuda::CUDAGuard guard(xs.device());
+  xs = xs.contiguous();
+  w = w.contiguous();
+  const int R = static_cast<int>(xs.size(0)), K = static_cast<int>(xs.size(1));
+  const int E = static_cast<int>(w.size(0)), N = static_cast<int>(w.size(1));
+  auto y = at::empty({R, N}, xs.options());
+  if (R == 0) return y;
+  const CUtensorMap* tw = tensor_map(w.data_ptr(), static_cast<uint64_t>(E) * N, K, K, 128);
+  const CUtensorMap* tx = tensor_map(xs.data_ptr(), R, K, K, ecz::grouped_block_n(R, E));
+  const int rc = ecz::launch_gemm_grouped(tw, tx, y.data_ptr(), offsets.data_ptr<int>(), E, R, N, K,
+                                          status_word(xs.device()), at::cuda::getCurrentCUDAStream());
+  TORCH_CHECK(rc == 0, "linear_grouped: K must be a multiple of 64 and N of 8");
+  return y;
+}
+
 // Explicit GEMM variant (tuning and benchmarks): mode 1 cluster split-K (DSMEM reduction), 2 split-K through a
 // global fp32 workspace reduced by the tile's last CTA, 3 persistent stream-K; splits <= 0 picks the default.
 Tensor linear_variant(Tensor x, Tensor w, int64_t mode, int64_t splits) {
@@ -651,6 +716,10 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
         py::arg("v_scale") = py::none());
   m.def("silu_mul", &silu_mul, "SwiGLU activation of [gate; up]");
   m.def("linear_parts", &linear_parts, "x @ w.T as bf16 or fp32 split-K partials for a fusing consumer");
+  m.def("moe_route", &moe_route, "top-k expert routing with deterministic expert-order positions");
+  m.def("moe_gather", &moe_gather, "permute token rows into expert order");
+  m.def("moe_combine", &moe_combine, "weighted sum of each token's expert outputs");
+  m.def("linear_grouped", &linear_grouped, "grouped expert GEMM over expert-ordered rows (tcgen05)");
   m.def("linear_variant", &linear_variant, "x @ w.T through an explicit GEMM variant (tuning)");
   m.def("gemm_cluster_capacity", &gemm_cluster_capacity, "resident clusters of the split-K cluster GEMM");
   m.def("raise_formatted", &raise_formatted, "raise a formatted RuntimeError (exception-path self test)");

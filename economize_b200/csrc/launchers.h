@@ -109,6 +109,16 @@ int gemm_wq_splits(int M, int N, int K, int fmt, int num_sms);
 int launch_gemm_wq(const WqMaps& maps, void* y, int M, int N, int K, int group, int fmt, int splits,
                    unsigned* status, cudaStream_t stream);
 
+// moe.cu: top-k routing, token permutation, grouped expert GEMM (weights stacked [E * N, K]) and weighted combine.
+int launch_moe_route(const void* logits, int T, int E, int k, int* ids, float* weights, int* pos, int* offsets,
+                     cudaStream_t stream);
+int launch_moe_gather(const void* x, const int* pos, void* xs, int T, int k, int H, cudaStream_t stream);
+int launch_moe_combine(const void* y, const int* pos, const float* w, void* out, int T, int k, int H,
+                       cudaStream_t stream);
+int grouped_block_n(int rows, int E);
+int launch_gemm_grouped(const CUtensorMap* tm_w, const CUtensorMap* tm_x, void* y, const int* offsets, int E,
+                        int rows, int N, int K, unsigned* status, cudaStream_t stream);
+
 // tmap.cpp: a 2-D tensor map over a row-major [rows, cols] matrix of 1- or 2-byte elements (elem_bytes), with a
 // {box_cols, box_rows} box and the given swizzle (0, 32, 64 or 128 bytes). Returns 0 on success.
 int make_tmap_2d(CUtensorMap* map, int elem_bytes, const void* base, uint64_t rows, uint64_t cols,

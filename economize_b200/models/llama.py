@@ -214,7 +214,8 @@ class CausalLM(nn.Module):
         if layer.router is not None:
             from ..parallel.moe import moe_mlp
 
-            return moe_mlp(x, layer.router, layer.w_gate_up, layer.w_down, self.config.experts_per_token)
+            return moe_mlp(x, layer.router, layer.w_gate_up, layer.w_down, self.config.experts_per_token,
+                           getattr(self, "ep", None))
         if self.observer is not None:
             self.observer(index, "w_gate_up", x)
         a = ops.silu_mul(self._linear(x, layer.w_gate_up))

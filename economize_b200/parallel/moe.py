@@ -1,0 +1,149 @@
+"""Sparse mixture-of-experts MLP (Mixtral-style top-k routing) on one GPU and with expert parallelism.
+
+One GPU (:func:`moe_mlp`): router GEMM -> ``moe_route`` (softmax, top-k, renormalised weights, expert-ordered
+positions) -> ``moe_gather`` -> grouped gate/up GEMM over all experts -> SwiGLU -> grouped down GEMM ->
+``moe_combine``; all on the device, no host synchronisation, so MoE decode steps record into CUDA graphs. The
+reference runs Hugging Face's MoE blocks (a Python loop over experts with a host-side ``nonzero`` per expert).
+
+Expert parallelism (:class:`ExpertParallel`): rank ``r`` of ``P`` owns experts ``[r E/P, (r+1) E/P)`` and every
+rank routes its own tokens. Dispatch and combine are all-to-all exchanges of the routed rows (``all_to_all_single``
+of the per-rank counts, then of the rows and their local expert ids; NCCL on GPUs, Gloo on the CPU); the rows a
+rank receives run through its experts and go back the same way, and the source rank sums each token's weighted
+expert outputs in fp32.
+"""
+
+from __future__ import annotations
+
+import torch
+import torch.distributed as dist
+import torch.nn.functional as F
+
+from .. import ops
+from ..errors import ConfigError
+
+__all__ = ["ExpertParallel", "moe_mlp", "moe_reference", "route", "shard_experts"]
+
+
+def route(logits: torch.Tensor, k: int) -> tuple[torch.Tensor, torch.Tensor]:
+    """Top-``k`` experts per row and their weights renormalised over the chosen ones (fp32; ties: lower id)."""
+    probs = torch.softmax(logits.float(), -1)
+    w, ids = torch.topk(probs, k, dim=-1, sorted=True)
+    return ids, w / w.sum(-1, keepdim=True)
+
+
+def moe_reference(x: torch.Tensor, router: torch.Tensor, w_gate_up: torch.Tensor, w_down: torch.Tensor,
+                  k: int) -> torch.Tensor:
+    """The MoE MLP in plain PyTorch (fp32 accumulation of the weighted expert outputs)."""
+    shape = x.shape
+    x2 = x.reshape(-1, shape[-1])
+    ids, w = route(F.linear(x2, router), k)
+    out = torch.zeros(x2.shape[0], shape[-1], dtype=torch.float32, device=x.device)
+    for e in range(w_gate_up.shape[0]):
+        rows, slot = (ids == e).nonzero(as_tuple=True)
+        if rows.numel() == 0:
+            continue
+        g, u = F.linear(x2[rows], w_gate_up[e]).chunk(2, -1)
+        y = F.linear(F.silu(g) * u, w_down[e])
+        out.index_add_(0, rows, y.float() * w[rows, slot][:, None])
+    return out.to(x.dtype).reshape(shape)
+
+
+def moe_mlp(x: torch.Tensor, router: torch.Tensor, w_gate_up: torch.Tensor, w_down: torch.Tensor,
+            k: int, ep: ExpertParallel | None = None) -> torch.Tensor:
+    """Top-``k`` MoE MLP of ``x [..., H]`` with experts ``w_gate_up [E, 2F, H]``, ``w_down [E, H, F]``."""
+    if ep is not None and ep.size > 1:
+        return ep.forward(x, router, w_gate_up, w_down, k)
+    if not x.is_cuda:
+        return moe_reference(x, router, w_gate_up, w_down, k)
+    from ..ops._ext import require
+
+    C = require()
+    shape = x.shape
+    x2 = x.reshape(-1, shape[-1]).contiguous()
+    logits = ops.linear(x2, router)
+    _, weights, pos, offsets = C.moe_route(logits, k)
+    xs = C.moe_gather(x2, pos)
+    a = ops.silu_mul(C.linear_grouped(xs, w_gate_up, offsets))
+    y = C.linear_grouped(a, w_down, offsets)
+    return C.moe_combine(y, pos, weights).reshape(shape)
+
+
+class ExpertParallel:
+    """Expert-parallel execution of a MoE layer over a process group (ranks own contiguous expert blocks).
+
+    Args:
+        rank, size: This rank and the group size.
+        group: The process group (NCCL on GPUs, Gloo on the CPU).
+    """
+
+    def __init__(self, rank: int, size: int, group=None) -> None:
+        self.rank, self.size, self.group = rank, size, group
+
+    def owned(self, num_experts: int) -> range:
+        if num_experts % self.size:
+            raise ConfigError(f"{num_experts} experts do not split over {self.size} ranks")
+        per = num_experts // self.size
+        return range(self.rank * per, (self.rank + 1) * per)
+
+    def _a2a(self, out: torch.Tensor, inp: torch.Tensor, out_splits: list[int], in_splits: list[int]) -> None:
+        dist.all_to_all_single(out, inp, out_splits, in_splits, group=self.group)
+
+    def forward(self, x: torch.Tensor, router: torch.Tensor, w_gate_up: torch.Tensor, w_down: torch.Tensor,
+                k: int) -> torch.Tensor:
+        """``w_gate_up``/``w_down`` hold this rank's experts only (``[E/P, 2F, H]``, ``[E/P, H, F]``); ``router``
+        covers all ``E`` experts."""
+        shape = x.shape
+        x2 = x.reshape(-1, shape[-1])
+        T, H = x2.shape
+        E = router.shape[0]
+        per = E // self.size
+        ids, w = route(ops.linear(x2, router), k)
+        flat = ids.reshape(-1)
+        order = torch.argsort(flat * (T * k) + torch.arange(T * k, device=x.device), stable=True)
+        dest = (flat // per)[order]
+        send_counts = torch.bincount(dest, minlength=self.size)
+        recv_counts = torch.empty_like(send_counts)
+        self._a2a(recv_counts, send_counts, [1] * self.size, [1] * self.size)
+        sc, rc = send_counts.tolist(), recv_counts.tolist()
+        rows = x2[order // k]
+        local_ids = (flat[order] - dest * per).to(torch.int64)
+        recv = torch.empty(sum(rc), H, dtype=x.dtype, device=x.device)
+        recv_ids = torch.empty(sum(rc), dtype=torch.int64, device=x.device)
+        self._a2a(recv, rows.contiguous(), rc, sc)
+        self._a2a(recv_ids, local_ids.contiguous(), rc, sc)
+        y = torch.empty_like(recv)
+        if recv.is_cuda and recv.shape[0]:  # this rank's experts as one grouped GEMM pair on the tensor cores
+            from ..ops._ext import require
+
+            C = require()
+            by_expert = torch.argsort(recv_ids, stable=True)
+            counts = torch.zeros(per, dtype=torch.int64, device=x.device).index_add_(
+                0, recv_ids, torch.ones_like(recv_ids))
+            offsets = torch.cat([counts.new_zeros(1), counts.cumsum(0)]).to(torch.int32)
+            a = ops.silu_mul(C.linear_grouped(recv[by_expert].contiguous(), w_gate_up, offsets))
+            y[by_expert] = C.linear_grouped(a, w_down, offsets)
+        else:
+            for e in range(per):  # experts of this rank
+                sel = (recv_ids == e).nonzero(as_tuple=True)[0]
+                if sel.numel() == 0:
+                    continue
+                g, u = F.linear(recv[sel], w_gate_up[e]).chunk(2, -1)
+                y[sel] = F.linear(F.silu(g) * u, w_down[e])
+        back = torch.empty_like(rows)
+        self._a2a(back, y, sc, rc)
+        out = torch.zeros(T, H, dtype=torch.float32, device=x.device)
+        weight = w.reshape(-1)[order]
+        out.index_add_(0, order // k, back.float() * weight[:, None])
+        return out.to(x.dtype).reshape(shape)
+
+
+def shard_experts(model, ep: ExpertParallel) -> None:
+    """Keep this rank's experts in every MoE layer of an engine model and attach ``ep``."""
+    with torch.no_grad():
+        for layer in model.layers:
+            if layer.router is None:
+                continue
+            own = ep.owned(layer.router.shape[0])
+            layer.w_gate_up = torch.nn.Parameter(layer.w_gate_up.data[own.start:own.stop].contiguous())
+            layer.w_down = torch.nn.Parameter(layer.w_down.data[own.start:own.stop].contiguous())
+    model.ep = ep
