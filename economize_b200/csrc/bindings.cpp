@@ -115,8 +115,8 @@ const CUtensorMap* tensor_map(const void* base, uint64_t rows, uint64_t cols, ui
 // returns (splits, the bf16 shape it stands for).
 std::pair<int, std::vector<int64_t>> parts_of(const Tensor& x) {
   if (x.scalar_type() == at::kBFloat16) return {0, x.sizes().vec()};
-  TORCH_CHECK(x.scalar_type() == at::kFloat && x.dim() >= 2 && x.is_contiguous(),
-              "expected a bf16 tensor or contiguous fp32 split-K partials [splits, ...]");
+  TORCH_CHECK(x.scalar_type() == at::kFloat && x.dim() >= 2 && x.is_contiguous() && x.size(0) <= 8,
+              "expected a bf16 tensor or contiguous fp32 split-K partials [splits <= 8, ...]");
   return {static_cast<int>(x.size(0)), std::vector<int64_t>(x.sizes().begin() + 1, x.sizes().end())};
 }
 
@@ -426,6 +426,41 @@ Tensor linear_grouped(Tensor xs, Tensor w, Tensor offsets) {
   return y;
 }
 
+// Block-scaled fp8 linear: x [M, K] bf16 is quantised per token and 128-wide K block, then multiplied with e4m3
+// weight codes [N, K] (uint8) whose fp32 scales are [N / 128, K / 128].
+Tensor linear_fp8(Tensor x, Tensor wq, Tensor sw, int64_t splits) {
+  CHECK_CUDA(x);
+  CHECK_BF16(x);
+  TORCH_CHECK(wq.scalar_type() == at::kByte && sw.scalar_type() == at::kFloat, "fp8 weights: uint8 codes, fp32 scales");
+  c10::cuda::CUDAGuard guard(x.device());
+  x = x.contiguous();
+  const int M = static_cast<int>(x.size(0)), K = static_cast<int>(x.size(1)), N = static_cast<int>(wq.size(0));
+  TORCH_CHECK(wq.size(1) == K && K % 128 == 0 && N % 128 == 0, "linear_fp8: K and N must be multiples of 128");
+  TORCH_CHECK(sw.size(0) == N / 128 && sw.size(1) == K / 128 && sw.is_contiguous(), "scales must be [N/128, K/128]");
+  auto y = at::empty({M, N}, x.options());
+  if (M == 0) return y;
+  cudaStream_t stream = at::cuda::getCurrentCUDAStream();
+  auto q = at::empty({M, K}, x.options().dtype(at::kByte));
+  auto sx = at::empty({K / 128, M}, x.options().dtype(at::kFloat));
+  TORCH_CHECK(ecz::launch_act_quant_fp8(x.data_ptr(), q.data_ptr(), sx.data_ptr<float>(), M, K, stream) == 0,
+              "activation quantisation failed");
+  const int bn = ecz::fp8_block_n(M);
+  const int sms = num_sms(x.get_device());
+  int sp = splits > 0 ? static_cast<int>(splits) : std::min(8, ecz::gemm_splits(M, N, K, bn <= 64 ? 2 * sms : sms));
+  const int total_kb = K / 128, kbps = (total_kb + sp - 1) / sp;
+  sp = (total_kb + kbps - 1) / kbps;
+  const CUtensorMap* tw = tensor_map_ex(wq.data_ptr(), 1, N, K, K, 128, 128, 128);
+  const CUtensorMap* tx = tensor_map_ex(q.data_ptr(), 1, M, K, K, 128, bn, 128);
+  const CUtensorMap* ts = tensor_map_ex(sx.data_ptr(), 4, K / 128, M, static_cast<uint64_t>(M) * 4, bn, 1, 0);
+  Tensor ws;
+  if (sp > 1) ws = at::empty({static_cast<int64_t>(sp) * M * N}, x.options().dtype(at::kFloat));
+  const int rc = ecz::launch_gemm_fp8(tw, tx, ts, sw.data_ptr<float>(), y.data_ptr(),
+                                      sp > 1 ? ws.data_ptr<float>() : nullptr, M, N, K, sp, status_word(x.device()),
+                                      stream);
+  TORCH_CHECK(rc == 0, "linear_fp8: launch failed (", rc, ")");
+  return y;
+}
+
 // Explicit GEMM variant (tuning and benchmarks): mode 1 cluster split-K (DSMEM reduction), 2 split-K through a
 // global fp32 workspace reduced by the tile's last CTA, 3 persistent stream-K; splits <= 0 picks the default.
 Tensor linear_variant(Tensor x, Tensor w, int64_t mode, int64_t splits) {
@@ -720,6 +755,8 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("moe_gather", &moe_gather, "permute token rows into expert order");
   m.def("moe_combine", &moe_combine, "weighted sum of each token's expert outputs");
   m.def("linear_grouped", &linear_grouped, "grouped expert GEMM over expert-ordered rows (tcgen05)");
+  m.def("linear_fp8", &linear_fp8, "block-scaled fp8 linear (1x128 activation / 128x128 weight scales)",
+        py::arg("x"), py::arg("wq"), py::arg("sw"), py::arg("splits") = 0);
   m.def("linear_variant", &linear_variant, "x @ w.T through an explicit GEMM variant (tuning)");
   m.def("gemm_cluster_capacity", &gemm_cluster_capacity, "resident clusters of the split-K cluster GEMM");
   m.def("raise_formatted", &raise_formatted, "raise a formatted RuntimeError (exception-path self test)");

@@ -25,15 +25,26 @@ struct Parts {
   long stride = 0;  // elements between consecutive partials
 };
 
+constexpr int kMaxParts = 8;  // the split-K GEMM feeding a consumer never splits wider
+
 __device__ __forceinline__ uint4 load8(const bf16* x, const Parts& parts, size_t off) {
   if (parts.p == nullptr) return *reinterpret_cast<const uint4*>(x + off);
-  float4 a = *reinterpret_cast<const float4*>(parts.p + off);
-  float4 b = *reinterpret_cast<const float4*>(parts.p + off + 4);
-  for (int s = 1; s < parts.splits; ++s) {
-    const float4 c = *reinterpret_cast<const float4*>(parts.p + s * parts.stride + off);
-    const float4 d = *reinterpret_cast<const float4*>(parts.p + s * parts.stride + off + 4);
-    a.x += c.x; a.y += c.y; a.z += c.z; a.w += c.w;
-    b.x += d.x; b.y += d.y; b.z += d.z; b.w += d.w;
+  // issue every partial's loads before the (ordered) sum
+  float4 c[kMaxParts], d[kMaxParts];
+#pragma unroll
+  for (int s = 0; s < kMaxParts; ++s) {
+    if (s < parts.splits) {
+      c[s] = __ldcg(reinterpret_cast<const float4*>(parts.p + s * parts.stride + off));
+      d[s] = __ldcg(reinterpret_cast<const float4*>(parts.p + s * parts.stride + off + 4));
+    }
+  }
+  float4 a = c[0], b = d[0];
+#pragma unroll
+  for (int s = 1; s < kMaxParts; ++s) {
+    if (s < parts.splits) {
+      a.x += c[s].x; a.y += c[s].y; a.z += c[s].z; a.w += c[s].w;
+      b.x += d[s].x; b.y += d[s].y; b.z += d[s].z; b.w += d[s].w;
+    }
   }
   __nv_bfloat162 h[4] = {__floats2bfloat162_rn(a.x, a.y), __floats2bfloat162_rn(a.z, a.w),
                          __floats2bfloat162_rn(b.x, b.y), __floats2bfloat162_rn(b.z, b.w)};
@@ -42,10 +53,15 @@ __device__ __forceinline__ uint4 load8(const bf16* x, const Parts& parts, size_t
 
 __device__ __forceinline__ __nv_bfloat162 load2(const bf16* x, const Parts& parts, size_t off) {
   if (parts.p == nullptr) return *reinterpret_cast<const __nv_bfloat162*>(x + off);
-  float2 a = *reinterpret_cast<const float2*>(parts.p + off);
-  for (int s = 1; s < parts.splits; ++s) {
-    const float2 c = *reinterpret_cast<const float2*>(parts.p + s * parts.stride + off);
-    a.x += c.x; a.y += c.y;
+  float2 c[kMaxParts];
+#pragma unroll
+  for (int s = 0; s < kMaxParts; ++s) {
+    if (s < parts.splits) c[s] = __ldcg(reinterpret_cast<const float2*>(parts.p + s * parts.stride + off));
+  }
+  float2 a = c[0];
+#pragma unroll
+  for (int s = 1; s < kMaxParts; ++s) {
+    if (s < parts.splits) { a.x += c[s].x; a.y += c[s].y; }
   }
   return __floats2bfloat162_rn(a.x, a.y);
 }
@@ -54,7 +70,7 @@ __device__ __forceinline__ __nv_bfloat162 load2(const bf16* x, const Parts& part
 // RMSNorm
 // ---------------------------------------------------------------------------------------------------------------
 template <int kMaxVec>
-__global__ void __launch_bounds__(256) rmsnorm_kernel(const bf16* __restrict__ x, const bf16* __restrict__ resid,
+__global__ void __launch_bounds__(512) rmsnorm_kernel(const bf16* __restrict__ x, const bf16* __restrict__ resid,
                                                       const bf16* __restrict__ w, bf16* __restrict__ out,
                                                       bf16* __restrict__ resid_out, int hidden, float eps,
                                                       Parts parts) {
@@ -124,7 +140,9 @@ int launch_rmsnorm(const void* x, const void* resid, const void* w, void* out, v
   const Parts parts{x_parts, splits, static_cast<long>(rows) * hidden};
   if (hidden % 8 != 0 || hidden > 256 * 8 * 8) return -1;
   const int nvec = hidden / 8;
-  int threads = nvec < 256 ? ((nvec + 31) / 32) * 32 : 256;
+  // partial sums cost several loads per vector: one vector per thread up to 512 threads
+  const int cap = x_parts != nullptr ? 512 : 256;
+  int threads = nvec < cap ? ((nvec + 31) / 32) * 32 : cap;
   const int per = (nvec + threads - 1) / threads;
   auto args = [&](auto kernel) {
     launch_pdl(kernel, dim3(rows), dim3(threads), 0, stream, static_cast<const bf16*>(x),

@@ -119,6 +119,13 @@ int grouped_block_n(int rows, int E);
 int launch_gemm_grouped(const CUtensorMap* tm_w, const CUtensorMap* tm_x, void* y, const int* offsets, int E,
                         int rows, int N, int K, unsigned* status, cudaStream_t stream);
 
+// gemm_fp8.cu: block-scaled fp8 GEMM (e4m3 weights [N, K] with fp32 scales [N / 128, K / 128]; activations
+// quantised per token and 128-wide K block by launch_act_quant_fp8 into codes [M, K] and scales [K / 128, M]).
+int fp8_block_n(int M);
+int launch_act_quant_fp8(const void* x, void* q, float* sx, int M, int K, cudaStream_t stream);
+int launch_gemm_fp8(const CUtensorMap* tm_w, const CUtensorMap* tm_x, const CUtensorMap* tm_sx, const float* sw,
+                    void* y, float* ws, int M, int N, int K, int splits, unsigned* status, cudaStream_t stream);
+
 // tmap.cpp: a 2-D tensor map over a row-major [rows, cols] matrix of 1- or 2-byte elements (elem_bytes), with a
 // {box_cols, box_rows} box and the given swizzle (0, 32, 64 or 128 bytes). Returns 0 on success.
 int make_tmap_2d(CUtensorMap* map, int elem_bytes, const void* base, uint64_t rows, uint64_t cols,

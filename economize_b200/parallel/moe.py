@@ -32,11 +32,12 @@ def route(logits: torch.Tensor, k: int) -> tuple[torch.Tensor, torch.Tensor]:
 
 
 def moe_reference(x: torch.Tensor, router: torch.Tensor, w_gate_up: torch.Tensor, w_down: torch.Tensor,
-                  k: int) -> torch.Tensor:
-    """The MoE MLP in plain PyTorch (fp32 accumulation of the weighted expert outputs)."""
+                  k: int, logits: torch.Tensor | None = None) -> torch.Tensor:
+    """The MoE MLP in plain PyTorch (fp32 accumulation of the weighted expert outputs); ``logits`` overrides the
+    router output (to route exactly like another implementation)."""
     shape = x.shape
     x2 = x.reshape(-1, shape[-1])
-    ids, w = route(F.linear(x2, router), k)
+    ids, w = route(F.linear(x2, router) if logits is None else logits, k)
     out = torch.zeros(x2.shape[0], shape[-1], dtype=torch.float32, device=x.device)
     for e in range(w_gate_up.shape[0]):
         rows, slot = (ids == e).nonzero(as_tuple=True)

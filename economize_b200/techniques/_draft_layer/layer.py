@@ -51,13 +51,15 @@ class DraftLayer(nn.Module):
     def run(self, x: torch.Tensor, residual: torch.Tensor, cache: KVCache,
             batch: StepBatch) -> tuple[torch.Tensor, torch.Tensor]:
         """``(mlp, a)`` for attention inputs ``x`` and residuals ``residual`` ``[B, T, *]``: the layer output is
-        ``a + mlp``, which the caller adds inside its next fused RMSNorm (the draft head's norm)."""
+        ``a + mlp``, which the caller adds inside its next fused RMSNorm (the draft head's norm); ``mlp`` may be
+        split-K :class:`~economize_b200.ops.Partials` that the norm reduces."""
         cos, sin = self.rope()
         k_cache, v_cache = cache.layer(0)
-        qkv = ops.linear(x, self.wqkv, self.bqkv)
+        qkv = ops.linear_parts(x, self.wqkv) if self.bqkv is None else ops.linear(x, self.wqkv, self.bqkv)
         q = ops.rope_store(qkv, batch.positions, cos, sin, self.heads, self.kv_heads, self.head_dim, k_cache,
                            v_cache, batch.kv_len, batch.n_new, None, None, self.eps, q_offset=batch.q_offset)
         o = ops.attention(q, k_cache, v_cache, batch.kv_len, batch.n_new, batch.mask, q_offset=batch.q_offset)
-        h = ops.linear(o.reshape(*o.shape[:2], -1), self.wo)
+        # split-K partials go straight into the consuming rope / norm / SwiGLU kernels
+        h = ops.linear_parts(o.reshape(*o.shape[:2], -1), self.wo)
         x2, a = ops.rmsnorm(h, self.post_norm, self.eps, residual)
-        return ops.linear(ops.silu_mul(ops.linear(x2, self.w_gate_up)), self.w_down), a
+        return ops.linear_parts(ops.silu_mul(ops.linear_parts(x2, self.w_gate_up)), self.w_down), a

@@ -18,7 +18,7 @@ from ...validation import check_choice, check_positive
 __all__ = ["DraftQuantConfig", "QUANT_FORMATS", "QUANT_METHODS_NAMES", "QuantConfig"]
 
 #: formats the packed kernel layout stores (economize also simulates int2/int3 and fp4 grids)
-QUANT_FORMATS = ("int4", "int8", "fp8")
+QUANT_FORMATS = ("int4", "int8", "fp8", "fp8_block")
 QUANT_METHODS_NAMES = ("rtn", "gptq", "awq")
 #: engine projection names and the Hugging Face module names fused into them
 PROJECTIONS = {"wqkv": ("self_attn.q_proj", "self_attn.k_proj", "self_attn.v_proj"), "wo": ("self_attn.o_proj",),
@@ -32,6 +32,8 @@ def _check_common(config) -> None:
         check_positive("group_size", config.group_size)
         if config.group_size % 64:
             raise ConfigError(f"group_size must be a multiple of 64 (the kernel's K tile), got {config.group_size}")
+    if config.format == "fp8_block":
+        return  # 128 x 128 weight blocks and 1 x 128 activation blocks are fixed by the format
     if config.format in ("int8", "fp8") and not config.symmetric:
         raise ConfigError(f"{config.format} weights are stored symmetric (no zero point): set symmetric=True")
 
@@ -41,7 +43,9 @@ class QuantConfig(TechniqueConfig):
     """Weight-only quantization of the target's decoder projections.
 
     Args:
-        format: ``"int4"`` (default, GPTQ/AWQ W4A16), ``"int8"`` (W8A16) or ``"fp8"`` (e4m3 weights).
+        format: ``"int4"`` (default, GPTQ/AWQ W4A16), ``"int8"`` (W8A16), ``"fp8"`` (e4m3 weights, bf16
+            activations) or ``"fp8_block"`` (W8A8: e4m3 weights with 128 x 128 block scales and activations
+            quantised per token and 128-wide block on the fly; ``group_size`` is ignored).
         method: ``"rtn"`` (round to nearest, no data), ``"gptq"`` (Hessian-aware error feedback, needs
             calibration tokens) or ``"awq"`` (activation-aware scaling folded into the preceding norm, then round
             to nearest with clipping search; needs calibration tokens).
@@ -85,7 +89,7 @@ class QuantConfig(TechniqueConfig):
             raise ConfigError(f"percdamp must lie in [0, 1], got {self.percdamp}")
         if any(int(i) < 1 for i in self.layers):
             raise ConfigError("layers are 1-indexed")
-        if self.method in ("gptq", "awq") and self.format == "fp8":
+        if self.method in ("gptq", "awq") and self.format in ("fp8", "fp8_block"):
             raise ConfigError(f"{self.method} fits integer grids; use method='rtn' for fp8")
         object.__setattr__(self, "targets", tuple(self.targets))
         object.__setattr__(self, "exclude", tuple(self.exclude))
@@ -101,8 +105,8 @@ class QuantConfig(TechniqueConfig):
         bad = [i for i in self.layers if i > n]
         if bad:
             raise ConfigError(f"layers {bad} exceed the model's {n} layers")
-        if model.config.is_moe:
-            raise ConfigError("weight-only quantization of MoE experts is not supported; use fp8 block scaling")
+        if model.config.is_moe and self.format != "fp8_block":
+            raise ConfigError("MoE models take format='fp8_block' (attention projections; experts stay bf16)")
 
 
 @dataclass(frozen=True)

@@ -15,6 +15,7 @@ from torch import nn
 
 from ...core.technique import Capability, Family, Technique, register_technique
 from ...errors import ConfigError
+from ...ops.fp8 import FP8BlockWeight
 from ...ops.quant import QWeight, install
 from . import methods
 from .config import PROJECTIONS, DraftQuantConfig, QuantConfig
@@ -45,8 +46,8 @@ class _QuantBase(Technique):
     def technique_state(self) -> dict[str, torch.Tensor]:
         out = {}
         for key, qw in self.weights.items():
-            for buf in ("qweight", "scales", "zeros"):
-                t = getattr(qw, buf)
+            for buf in ("codes", "qweight", "scales", "zeros"):
+                t = getattr(qw, buf, None)
                 if t is not None:
                     out[f"weights.{key}.{buf}"] = t.detach()
         for key, t in self.replaced.items():
@@ -66,6 +67,9 @@ class _QuantBase(Technique):
                 raise ConfigError(f"{self.name}: unexpected tensor {name}")
         self.weights = nn.ModuleDict()
         for key, bufs in found.items():
+            if "codes" in bufs:
+                self.weights[key] = FP8BlockWeight(bufs["codes"], bufs["scales"], self._dtype())
+                continue
             k_in = bufs["qweight"].shape[1] * (2 if cfg.format == "int4" else 1)
             group = cfg.group_size or k_in
             self.weights[key] = QWeight(bufs["qweight"], bufs["scales"], bufs.get("zeros"), cfg.format, group,
@@ -104,8 +108,14 @@ class QuantTechnique(_QuantBase):
             for n, hf in PROJECTIONS.items():
                 if not _selected(hf, cfg.targets, cfg.exclude):
                     continue
-                k = getattr(self.model.layers[i], n).shape[1]
-                if k % 64 or (cfg.group_size and k % cfg.group_size):
+                w = getattr(self.model.layers[i], n)
+                if w.dim() != 2:  # stacked MoE experts
+                    self.skipped.append(f"layers.{i}.{n}")
+                    continue
+                k = w.shape[1]
+                block = cfg.format == "fp8_block"
+                if (block and (k % 128 or w.shape[0] % 128)) or \
+                        (not block and (k % 64 or (cfg.group_size and k % cfg.group_size))):
                     self.skipped.append(f"layers.{i}.{n}")
                     continue
                 names.append(n)
@@ -136,6 +146,9 @@ class QuantTechnique(_QuantBase):
             layer = model.layers[i]
             for name in names:
                 w = getattr(layer, name).detach()
+                if cfg.format == "fp8_block":
+                    self.weights[_key(i, name)] = FP8BlockWeight.from_weight(w)
+                    continue
                 if cfg.method == "gptq":
                     qw = methods.gptq(w, stats[(i, name)].hessian, cfg.format, cfg.group_size, cfg.symmetric,
                                       cfg.blocksize, cfg.percdamp, cfg.act_order)

@@ -108,7 +108,10 @@ def test_moe_kernels_match_reference(cuda, T, E, k, H, F):
     gu = (torch.randn(E, 2 * F, H, device=cuda, generator=g) * 0.02).bfloat16()
     down = (torch.randn(E, H, F, device=cuda, generator=g) * 0.02).bfloat16()
     out = moe_mlp(x, router, gu, down, k)
-    exp = moe_reference(x.float(), router.float(), gu.float(), down.float(), k)
+    from economize_b200 import ops
+
+    logits = ops.linear(x, router).float()  # route like the kernel path (bf16 router logits)
+    exp = moe_reference(x.float(), router.float(), gu.float(), down.float(), k, logits=logits)
     torch.testing.assert_close(out.float(), exp, atol=3e-2, rtol=3e-2)
 
 

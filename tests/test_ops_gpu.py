@@ -260,3 +260,13 @@ def test_consumers_reduce_partials_exactly(cuda):
         outs.append((q, kc, vc))
     for u, v in zip(*outs):
         assert torch.equal(u, v)
+
+
+def test_partials_index_like_the_dense_tensor(cuda):
+    g = torch.Generator(device=cuda).manual_seed(2)
+    x = torch.randn(2, 9, 4096, device=cuda, generator=g).bfloat16()
+    w = (torch.randn(4096, 4096, device=cuda, generator=g) * 0.02).bfloat16()
+    p = ops.linear_parts(x, w)
+    assert isinstance(p, ops.Partials)
+    rows, cols = torch.tensor([0, 1], device=cuda), torch.tensor([3, 8], device=cuda)
+    assert torch.equal(p[rows, cols].sum(), p.sum()[rows, cols])

@@ -166,3 +166,44 @@ def test_quantized_model_decodes_on_gpu(cuda):
     plain = eff.decode(p, 16, decoding=eco.DecodeConfig(cycle_length=1)).tokens
     spec = eff.decode(p, 16).tokens
     assert torch.equal(spec.cpu(), plain.cpu())
+
+
+def test_fp8_block_reference_roundtrip():
+    from economize_b200.ops.fp8 import FP8BlockWeight, quantize_activations
+
+    g = torch.Generator().manual_seed(0)
+    w = torch.randn(256, 384, generator=g) * 0.02
+    fw = FP8BlockWeight.from_weight(w)
+    assert fw.codes.dtype == torch.uint8 and fw.scales.shape == (2, 3)
+    assert (fw.dequantize(torch.float32) - w).norm() / w.norm() < 0.04
+    x = torch.randn(5, 384, generator=g)
+    q, s = quantize_activations(x)
+    assert s.shape == (5, 3) and ((q.abs() <= 448).all())
+    y = fw.linear(x)
+    assert (y - x @ w.t()).norm() / (x @ w.t()).norm() < 0.06
+
+
+def test_fp8_block_technique_decodes():
+    model = tiny_model()
+    eff = eco.apply(model, QuantConfig(format="fp8_block"))
+    from economize_b200.ops.fp8 import FP8BlockWeight
+
+    assert isinstance(eff.model.layers[0].wqkv, FP8BlockWeight)
+    p = prompts((14,))[0]
+    assert torch.equal(eff.decode(p, 6).tokens, reference_greedy(eff.model, p, 6))
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("M,N,K", [(1, 4096, 4096), (61, 6144, 4096), (100, 1024, 14336), (7, 256, 512)])
+def test_linear_fp8_matches_reference(cuda, M, N, K):
+    from economize_b200.ops.fp8 import FP8BlockWeight, quantize_activations
+
+    g = torch.Generator(device=cuda).manual_seed(0)
+    w = torch.randn(N, K, device=cuda, generator=g) * 0.02
+    fw = FP8BlockWeight.from_weight(w)
+    x = torch.randn(M, K, device=cuda, generator=g).bfloat16()
+    y = fw.linear(x)
+    q, s = quantize_activations(x)
+    xd = (q.reshape(M, -1, 128) * s[..., None]).reshape(M, K)
+    exact = xd @ fw.dequantize(torch.float32).t()
+    torch.testing.assert_close(y.float(), exact, atol=2e-2, rtol=2e-2)
