@@ -441,8 +441,10 @@ Tensor linear_fp8(Tensor x, Tensor wq, Tensor sw, int64_t splits) {
   if (M == 0) return y;
   cudaStream_t stream = at::cuda::getCurrentCUDAStream();
   auto q = at::empty({M, K}, x.options().dtype(at::kByte));
-  auto sx = at::empty({K / 128, M}, x.options().dtype(at::kFloat));
-  TORCH_CHECK(ecz::launch_act_quant_fp8(x.data_ptr(), q.data_ptr(), sx.data_ptr<float>(), M, K, stream) == 0,
+  const int sx_stride = (M + 3) / 4 * 4;  // TMA rows must be 16-byte multiples
+  auto sx = at::empty({K / 128, sx_stride}, x.options().dtype(at::kFloat));
+  TORCH_CHECK(ecz::launch_act_quant_fp8(x.data_ptr(), q.data_ptr(), sx.data_ptr<float>(), M, K, sx_stride, stream) ==
+                  0,
               "activation quantisation failed");
   const int bn = ecz::fp8_block_n(M);
   const int sms = num_sms(x.get_device());
@@ -451,7 +453,7 @@ Tensor linear_fp8(Tensor x, Tensor wq, Tensor sw, int64_t splits) {
   sp = (total_kb + kbps - 1) / kbps;
   const CUtensorMap* tw = tensor_map_ex(wq.data_ptr(), 1, N, K, K, 128, 128, 128);
   const CUtensorMap* tx = tensor_map_ex(q.data_ptr(), 1, M, K, K, 128, bn, 128);
-  const CUtensorMap* ts = tensor_map_ex(sx.data_ptr(), 4, K / 128, M, static_cast<uint64_t>(M) * 4, bn, 1, 0);
+  const CUtensorMap* ts = tensor_map_ex(sx.data_ptr(), 4, K / 128, M, static_cast<uint64_t>(sx_stride) * 4, bn, 1, 0);
   Tensor ws;
   if (sp > 1) ws = at::empty({static_cast<int64_t>(sp) * M * N}, x.options().dtype(at::kFloat));
   const int rc = ecz::launch_gemm_fp8(tw, tx, ts, sw.data_ptr<float>(), y.data_ptr(),
@@ -459,6 +461,29 @@ Tensor linear_fp8(Tensor x, Tensor wq, Tensor sw, int64_t splits) {
                                       stream);
   TORCH_CHECK(rc == 0, "linear_fp8: launch failed (", rc, ")");
   return y;
+}
+
+// Top-k log-probabilities of fp32 logit rows [..., V] and their (optionally draft-to-target mapped) ids.
+std::tuple<Tensor, Tensor> topk_logp(Tensor logits, int64_t k, double floor_v, c10::optional<Tensor> d2t) {
+  CHECK_CUDA(logits);
+  TORCH_CHECK(logits.scalar_type() == at::kFloat, "topk_logp takes fp32 logits");
+  c10::cuda::CUDAGuard guard(logits.device());
+  logits = logits.contiguous();
+  const int V = static_cast<int>(logits.size(-1));
+  const int rows = static_cast<int>(logits.numel() / V);
+  std::vector<int64_t> shape(logits.sizes().begin(), logits.sizes().end());
+  shape.back() = k;
+  auto vals = at::empty(shape, logits.options());
+  auto ids = at::empty(shape, logits.options().dtype(at::kLong));
+  if (d2t.has_value()) {
+    CHECK_I64(*d2t);
+    TORCH_CHECK(d2t->numel() == V, "d2t must have one entry per logit");
+  }
+  const int rc = ecz::launch_topk_logp(logits.data_ptr<float>(), d2t.has_value() ? d2t->data_ptr<int64_t>() : nullptr,
+                                       vals.data_ptr<float>(), ids.data_ptr<int64_t>(), rows, V, static_cast<int>(k),
+                                       static_cast<float>(floor_v), at::cuda::getCurrentCUDAStream());
+  TORCH_CHECK(rc == 0, "topk_logp: 1 <= k <= 16");
+  return {vals, ids};
 }
 
 // Explicit GEMM variant (tuning and benchmarks): mode 1 cluster split-K (DSMEM reduction), 2 split-K through a
@@ -757,6 +782,8 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("linear_grouped", &linear_grouped, "grouped expert GEMM over expert-ordered rows (tcgen05)");
   m.def("linear_fp8", &linear_fp8, "block-scaled fp8 linear (1x128 activation / 128x128 weight scales)",
         py::arg("x"), py::arg("wq"), py::arg("sw"), py::arg("splits") = 0);
+  m.def("topk_logp", &topk_logp, "fused log-softmax + top-k (+ draft-to-target id map)", py::arg("logits"),
+        py::arg("k"), py::arg("floor"), py::arg("d2t") = py::none());
   m.def("linear_variant", &linear_variant, "x @ w.T through an explicit GEMM variant (tuning)");
   m.def("gemm_cluster_capacity", &gemm_cluster_capacity, "resident clusters of the split-K cluster GEMM");
   m.def("raise_formatted", &raise_formatted, "raise a formatted RuntimeError (exception-path self test)");

@@ -210,7 +210,7 @@ __global__ void __launch_bounds__(256) fp8_reduce_kernel(const float* __restrict
 
 // one warp per (token, K-block): 128 values, 4 per lane
 __global__ void __launch_bounds__(256) act_quant_kernel(const bf16* __restrict__ x, uint8_t* __restrict__ q,
-                                                        float* __restrict__ sx, int M, int K) {
+                                                        float* __restrict__ sx, int M, int K, int sx_stride) {
   pdl_trigger();
   pdl_wait();
   const int warp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5, lane = threadIdx.x & 31;
@@ -228,7 +228,7 @@ __global__ void __launch_bounds__(256) act_quant_kernel(const bf16* __restrict__
   const __nv_fp8x2_storage_t hi = __nv_cvt_float2_to_fp8x2(make_float2(__fdiv_rn(b.x, scale), __fdiv_rn(b.y, scale)),
                                                            __NV_SATFINITE, __NV_E4M3);
   *reinterpret_cast<uint32_t*>(q + off) = static_cast<uint32_t>(lo) | (static_cast<uint32_t>(hi) << 16);
-  if (lane == 0) sx[static_cast<size_t>(kb) * M + m] = scale;
+  if (lane == 0) sx[static_cast<size_t>(kb) * sx_stride + m] = scale;
 }
 
 template <int BN>
@@ -259,11 +259,11 @@ int run_fp8(const CUtensorMap& tm_w, const CUtensorMap& tm_x, const CUtensorMap&
 
 int fp8_block_n(int M) { return M <= 32 ? 32 : (M <= 64 ? 64 : 128); }
 
-int launch_act_quant_fp8(const void* x, void* q, float* sx, int M, int K, cudaStream_t stream) {
-  if (K % kBK != 0) return -1;
+int launch_act_quant_fp8(const void* x, void* q, float* sx, int M, int K, int sx_stride, cudaStream_t stream) {
+  if (K % kBK != 0 || sx_stride < M) return -1;
   const long warps = static_cast<long>(M) * (K / kBK);
   launch_pdl(act_quant_kernel, dim3(static_cast<unsigned>((warps * 32 + 255) / 256)), dim3(256), 0, stream,
-             static_cast<const bf16*>(x), static_cast<uint8_t*>(q), sx, M, K);
+             static_cast<const bf16*>(x), static_cast<uint8_t*>(q), sx, M, K, sx_stride);
   return 0;
 }
 

@@ -81,6 +81,8 @@ int launch_attention(const void* q, const CUtensorMap* tm_k, const CUtensorMap* 
                      const float* v_scale = nullptr);
 
 // sampling.cu
+int launch_topk_logp(const float* logits, const int64_t* d2t, float* vals, int64_t* ids, int rows, int V, int k,
+                     float floor_v, cudaStream_t stream);
 int launch_sample(const float* probs, const float* u, int64_t* out, int rows, int V, cudaStream_t stream);
 int launch_rejection(const float* p, const float* q, const int64_t* drafts, const float* u_acc, const float* u_draw,
                      int* n_acc, int64_t* out, int B, int k, int V, cudaStream_t stream);
@@ -120,9 +122,10 @@ int launch_gemm_grouped(const CUtensorMap* tm_w, const CUtensorMap* tm_x, void* 
                         int rows, int N, int K, unsigned* status, cudaStream_t stream);
 
 // gemm_fp8.cu: block-scaled fp8 GEMM (e4m3 weights [N, K] with fp32 scales [N / 128, K / 128]; activations
-// quantised per token and 128-wide K block by launch_act_quant_fp8 into codes [M, K] and scales [K / 128, M]).
+// quantised per token and 128-wide K block by launch_act_quant_fp8 into codes [M, K] and scales [K / 128, >= M]).
 int fp8_block_n(int M);
-int launch_act_quant_fp8(const void* x, void* q, float* sx, int M, int K, cudaStream_t stream);
+// sx rows are `sx_stride` floats apart (>= M, a multiple of 4 so that a TMA map can read them).
+int launch_act_quant_fp8(const void* x, void* q, float* sx, int M, int K, int sx_stride, cudaStream_t stream);
 int launch_gemm_fp8(const CUtensorMap* tm_w, const CUtensorMap* tm_x, const CUtensorMap* tm_sx, const float* sw,
                     void* y, float* ws, int M, int N, int K, int splits, unsigned* status, cudaStream_t stream);
 

@@ -133,6 +133,98 @@ __global__ void __launch_bounds__(kThreads) rejection_kernel(const float* __rest
   }
 }
 
+// ---- fused log-softmax + top-k (draft-tree expansion) -----------------------------------------------------------
+// One CTA per row of logits [R, V] (fp32): max and sum of exponentials, then the k largest logits (ties: lower
+// index) from per-thread lists merged by warps and then by warp 0. Outputs log-probabilities
+// max(logit - logsumexp, floor) and indices mapped to target ids (index + d2t[index] when a draft vocabulary map is
+// given). Replaces log_softmax + clamp + topk + gather in every expansion step of the dynamic tree.
+constexpr int kTopThreads = 512;
+constexpr int kMaxTopK = 16;
+
+struct Cand {
+  float v;
+  int i;
+};
+
+__device__ __forceinline__ bool better(const Cand& a, const Cand& b) { return a.v > b.v || (a.v == b.v && a.i < b.i); }
+
+__global__ void __launch_bounds__(kTopThreads) topk_logp_kernel(const float* __restrict__ logits,
+                                                               const int64_t* __restrict__ d2t, float* __restrict__ vals,
+                                                               int64_t* __restrict__ ids, int V, int k, float floor_v) {
+  pdl_trigger();
+  pdl_wait();
+  const float* row = logits + static_cast<size_t>(blockIdx.x) * V;
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  __shared__ float red[32];
+  __shared__ Cand wl[kTopThreads / 32][kMaxTopK];
+  // max
+  float mx = -INFINITY;
+  for (int i = tid; i < V; i += kTopThreads) mx = fmaxf(mx, row[i]);
+  mx = warp_max(mx);
+  if (lane == 0) red[warp] = mx;
+  __syncthreads();
+  if (warp == 0) {
+    float t = lane < kTopThreads / 32 ? red[lane] : -INFINITY;
+    t = warp_max(t);
+    if (lane == 0) red[0] = t;
+  }
+  __syncthreads();
+  mx = red[0];
+  __syncthreads();
+  // sum of exponentials and the thread's own top-k (sorted, descending)
+  Cand mine[kMaxTopK];
+  for (int j = 0; j < k; ++j) mine[j] = {-INFINITY, 0x7fffffff};
+  float se = 0.f;
+  for (int i = tid; i < V; i += kTopThreads) {
+    const float x = row[i];
+    se += __expf(x - mx);
+    Cand c{x, i};
+    if (better(c, mine[k - 1])) {
+      int j = k - 1;
+      while (j > 0 && better(c, mine[j - 1])) {
+        mine[j] = mine[j - 1];
+        --j;
+      }
+      mine[j] = c;
+    }
+  }
+  se = warp_sum(se);
+  if (lane == 0) red[warp] = se;
+  // warp merge: k rounds of the best head among the 32 lanes' lists
+  int head = 0;
+  for (int r = 0; r < k; ++r) {
+    Cand c = head < k ? mine[head] : Cand{-INFINITY, 0x7fffffff};
+    Cand best = c;
+    for (int off = 16; off > 0; off >>= 1) {
+      Cand o{__shfl_xor_sync(0xffffffffu, best.v, off), __shfl_xor_sync(0xffffffffu, best.i, off)};
+      if (better(o, best)) best = o;
+    }
+    if (head < k && c.i == best.i && c.v == best.v) ++head;
+    if (lane == 0) wl[warp][r] = best;
+  }
+  __syncthreads();
+  if (warp == 0) {
+    float tot = lane < kTopThreads / 32 ? red[lane] : 0.f;
+    tot = warp_sum(tot);
+    const float lse = mx + __logf(tot);
+    int h = 0;  // lane l merges list l (16 lists of k)
+    for (int r = 0; r < k; ++r) {
+      Cand c = (lane < kTopThreads / 32 && h < k) ? wl[lane][h] : Cand{-INFINITY, 0x7fffffff};
+      Cand best = c;
+      for (int off = 16; off > 0; off >>= 1) {
+        Cand o{__shfl_xor_sync(0xffffffffu, best.v, off), __shfl_xor_sync(0xffffffffu, best.i, off)};
+        if (better(o, best)) best = o;
+      }
+      if (lane < kTopThreads / 32 && h < k && c.i == best.i && c.v == best.v) ++h;
+      if (lane == 0) {
+        const size_t o = static_cast<size_t>(blockIdx.x) * k + r;
+        vals[o] = fmaxf(best.v - lse, floor_v);
+        ids[o] = d2t != nullptr ? best.i + d2t[best.i] : best.i;
+      }
+    }
+  }
+}
+
 }  // namespace
 
 int launch_sample(const float* probs, const float* u, int64_t* out, int rows, int V, cudaStream_t stream) {
@@ -145,6 +237,14 @@ int launch_rejection(const float* p, const float* q, const int64_t* drafts, cons
                      int* n_acc, int64_t* out, int B, int k, int V, cudaStream_t stream) {
   if (B == 0) return 0;
   launch_pdl(rejection_kernel, dim3(B), dim3(kThreads), 0, stream, p, q, drafts, u_acc, u_draw, n_acc, out, k, V);
+  return 0;
+}
+
+int launch_topk_logp(const float* logits, const int64_t* d2t, float* vals, int64_t* ids, int rows, int V, int k,
+                     float floor_v, cudaStream_t stream) {
+  if (k < 1 || k > kMaxTopK || k > V) return -1;
+  if (rows == 0) return 0;
+  launch_pdl(topk_logp_kernel, dim3(rows), dim3(kTopThreads), 0, stream, logits, d2t, vals, ids, V, k, floor_v);
   return 0;
 }
 

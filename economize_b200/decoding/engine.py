@@ -477,10 +477,14 @@ class SpecEngine:
         drafter, tree = self.drafter, self.tree
         batch, dev = st.batch, st.kv_len.device
         k, depth = tree.topk, tree.depth
-        logp = torch.log_softmax(st.root_logits, -1).clamp_min(LOGP_FLOOR)
-        top = logp.topk(k, -1)
-        f_tokens = drafter.to_target(top.indices)  # frontier tokens [B, k]
-        f_scores = top.values
+        # fused log-softmax + top-k (+ draft-to-target id map) per expansion: one kernel per step
+        d2t = getattr(drafter, "d2t_map", None)
+
+        def expand(logits: torch.Tensor) -> tuple[torch.Tensor, torch.Tensor]:
+            vals, ids = ops.topk_logp(logits, k, LOGP_FLOOR, d2t)
+            return vals, (ids if d2t is not None else drafter.to_target(ids))
+
+        f_scores, f_tokens = expand(st.root_logits)  # frontier tokens [B, k]
         f_cand = torch.arange(k, device=dev).expand(batch, k)
         cand_tokens, cand_scores = [f_tokens], [f_scores]
         cand_parents = [torch.full((batch, k), -1, dtype=torch.int64, device=dev)]
@@ -498,10 +502,9 @@ class SpecEngine:
             fwd_bits[:, (d - 1) * k: d * k] = bits
             pos = (st.kv_len + d).to(torch.int32)[:, None].expand(batch, k).contiguous()
             logits, outs = drafter.tree_step(f_tokens, states, pos, base, d * k, (d - 1) * k, bits)
-            clp = torch.log_softmax(logits, -1).clamp_min(LOGP_FLOOR)
-            ctop = clp.topk(k, -1)
-            child_scores = (f_scores[:, :, None] + ctop.values).reshape(batch, k * k)
-            child_tokens = drafter.to_target(ctop.indices).reshape(batch, k * k)
+            c_vals, c_ids = expand(logits)
+            child_scores = (f_scores[:, :, None] + c_vals).reshape(batch, k * k)
+            child_tokens = c_ids.reshape(batch, k * k)
             child_parents = f_cand[:, :, None].expand(batch, k, k).reshape(batch, k * k)
             cand_tokens.append(child_tokens)
             cand_scores.append(child_scores)

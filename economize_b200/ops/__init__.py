@@ -31,6 +31,7 @@ __all__ = [
     "rejection",
     "rope_store",
     "sample",
+    "topk_logp",
     "silu_mul",
 ]
 
@@ -195,3 +196,15 @@ def ngram(history: torch.Tensor, length: torch.Tensor, k: int, min_n: int, max_n
     if history.is_cuda:
         return require().ngram(history, length.to(torch.int32), int(k), int(min_n), int(max_n), bool(earliest))
     return reference.ngram(history, length, k, min_n, max_n, earliest)
+
+
+def topk_logp(logits: torch.Tensor, k: int, floor: float, d2t: torch.Tensor | None = None
+              ) -> tuple[torch.Tensor, torch.Tensor]:
+    """``k`` largest log-probabilities of every row of ``logits [..., V]`` (clamped below at ``floor``; ties: lower
+    index) and their indices, mapped to target ids by ``index + d2t[index]`` when ``d2t`` is given."""
+    if logits.is_cuda:
+        return require().topk_logp(logits.float(), int(k), float(floor), d2t)
+    logp = torch.log_softmax(logits.float(), -1).clamp_min(floor)
+    top = logp.topk(k, -1)
+    idx = top.indices
+    return top.values, (idx + d2t[idx] if d2t is not None else idx)

@@ -166,6 +166,11 @@ class Eagle3Drafter:
         self.carry_size = technique.model.config.hidden_size
         self.cache: KVCache | None = None
 
+    @property
+    def d2t_map(self) -> torch.Tensor:
+        """Draft id -> target id offsets (read by the engine's fused top-k)."""
+        return self.t.d2t
+
     def begin(self, batch: int, capacity: int) -> None:
         layer = self.t.layer
         if self.cache is None or self.cache.batch != batch or self.cache.capacity < capacity:

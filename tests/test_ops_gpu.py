@@ -270,3 +270,14 @@ def test_partials_index_like_the_dense_tensor(cuda):
     assert isinstance(p, ops.Partials)
     rows, cols = torch.tensor([0, 1], device=cuda), torch.tensor([3, 8], device=cuda)
     assert torch.equal(p[rows, cols].sum(), p.sum()[rows, cols])
+
+
+@pytest.mark.parametrize("rows,V,k", [(1, 32000, 10), (10, 32000, 10), (61, 1024, 16), (3, 128256, 4)])
+def test_topk_logp_matches_torch(cuda, rows, V, k):
+    g = torch.Generator(device=cuda).manual_seed(0)
+    logits = torch.randn(rows, V, device=cuda, generator=g) * 3
+    d2t = torch.randint(0, 5, (V,), device=cuda, generator=g)
+    vals, ids = ops.topk_logp(logits, k, -1e4, d2t)
+    ref = torch.log_softmax(logits, -1).topk(k, -1)
+    _close(vals, ref.values, 1e-4, 1e-5)
+    assert torch.equal(ids, ref.indices + d2t[ref.indices])

@@ -194,7 +194,8 @@ def test_fp8_block_technique_decodes():
 
 
 @pytest.mark.gpu
-@pytest.mark.parametrize("M,N,K", [(1, 4096, 4096), (61, 6144, 4096), (100, 1024, 14336), (7, 256, 512)])
+@pytest.mark.parametrize("M,N,K", [(1, 4096, 4096), (61, 6144, 4096), (100, 1024, 14336), (7, 256, 512),
+                                   (100, 256, 512), (33, 512, 1024)])
 def test_linear_fp8_matches_reference(cuda, M, N, K):
     from economize_b200.ops.fp8 import FP8BlockWeight, quantize_activations
 
