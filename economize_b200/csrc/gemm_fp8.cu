@@ -156,6 +156,8 @@ __global__ void __launch_bounds__(kThreads, Fp8Cfg<BN>::kOcc)
     for (int kb = 0; kb < nkb; ++kb) {
       const int s = kb % S, b = kb & 1;
       if (!mbar_wait(&acc_full[b], (kb >> 1) & 1u, status, kStatusWaitAccum, abort_flag)) break;
+      // the stage's activation scales were written by TMA: acquire them through the stage's own barrier
+      if (!mbar_wait(&full[s], (kb / S) & 1u, status, kStatusWaitFull, abort_flag)) break;
       tc_fence_after();
       const float wscale = sw[static_cast<size_t>(n_blk) * total_kb + kb0 + kb];
       const float* sx = s_tiles + s * (Cfg::kScaleBytes / 4);
