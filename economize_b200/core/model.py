@@ -214,20 +214,35 @@ class EfficientModel(nn.Module):
 def build_model(model: nn.Module, configs: Sequence[TechniqueConfig], *, decoding: DecodeConfig | None = None,
                 calibration: Any = None, states: dict[str, dict[str, torch.Tensor]] | None = None) -> EfficientModel:
     engine_model = as_engine_model(model)
-    techniques = [technique_for(c)(c, engine_model) for c in configs]
-    techniques.sort(key=_rank)
-    check_compatible(techniques)
     digest = None
-    if any(Capability.WEIGHTS in t.capabilities for t in techniques):
+    if any(Capability.WEIGHTS in technique_for(c).capabilities for c in configs):
         from .serialization import teacher_fingerprint
 
         digest = teacher_fingerprint(engine_model)
-    for t in techniques:
+
+    def build(config):
+        t = technique_for(config)(config, engine_model)
         if states and t.name in states:
             t.load_technique_state(states[t.name])
         if hasattr(t, "calibrate") and calibration is not None:
             t.calibrate(calibration)
+        return t
+
+    # weight transforms (which may change the depth or the projections) are built and attached first, so the other
+    # techniques are built against the transformed model
+    order = sorted(configs, key=lambda c: _rank(technique_for(c)))
+    techniques: list[Technique] = []
+    for config in order:
+        if Capability.WEIGHTS in technique_for(config).capabilities:
+            t = build(config)
+            techniques.append(t)
+            check_compatible(techniques)
+            t.attach()
+    rest = [build(c) for c in order if Capability.WEIGHTS not in technique_for(c).capabilities]
+    check_compatible(techniques + rest)
+    for t in rest:
         t.attach()
+    techniques += rest
     for t in techniques:  # drafter transforms (draft_quant, frspec) act once the drafter is attached
         if hasattr(t, "after_drafter"):
             drafter = next((d for d in techniques if Capability.DRAFTER in d.capabilities), None)

@@ -486,6 +486,33 @@ std::tuple<Tensor, Tensor> topk_logp(Tensor logits, int64_t k, double floor_v, c
   return {vals, ids};
 }
 
+// 2:4 sparse linear: kept bf16 values [N, K / 2] and their positions [N / 2, K / 4] (uint8), expanded to dense
+// tiles in shared memory by the weight-streaming GEMM.
+Tensor linear_sp24(Tensor x, Tensor values, Tensor meta, int64_t splits) {
+  CHECK_CUDA(x);
+  CHECK_BF16(x);
+  CHECK_BF16(values);
+  TORCH_CHECK(meta.scalar_type() == at::kByte, "2:4 positions must be uint8");
+  c10::cuda::CUDAGuard guard(x.device());
+  x = x.contiguous();
+  const int M = static_cast<int>(x.size(0)), K = static_cast<int>(x.size(1)), N = static_cast<int>(values.size(0));
+  TORCH_CHECK(values.size(1) == K / 2 && values.is_contiguous(), "values must be [N, K / 2]");
+  TORCH_CHECK(meta.size(0) == N / 2 && meta.size(1) == K / 4 && meta.is_contiguous(), "positions must be [N/2, K/4]");
+  TORCH_CHECK(K % 64 == 0 && N % 8 == 0, "linear_sp24: K must be a multiple of 64, N of 8");
+  auto y = at::empty({M, N}, x.options());
+  if (M == 0) return y;
+  ecz::WqMaps maps;
+  maps.w = tensor_map_ex(values.data_ptr(), 2, N, K / 2, static_cast<uint64_t>(K), 32, 128, 0);
+  maps.s = tensor_map_ex(meta.data_ptr(), 1, N / 2, K / 4, static_cast<uint64_t>(K / 4), 16, 64, 0);
+  maps.x = tensor_map(x.data_ptr(), M, K, K, ecz::gemm_block_n(M));
+  const int sp = splits > 0 ? static_cast<int>(splits)
+                            : ecz::gemm_wq_splits(M, N, K, ecz::kWqInt8, num_sms(x.get_device()));
+  const int rc = ecz::launch_gemm_wq(maps, y.data_ptr(), M, N, K, K, ecz::kWqSp24, sp, status_word(x.device()),
+                                     at::cuda::getCurrentCUDAStream());
+  TORCH_CHECK(rc == 0, "linear_sp24: launch failed (", rc, ")");
+  return y;
+}
+
 // Explicit GEMM variant (tuning and benchmarks): mode 1 cluster split-K (DSMEM reduction), 2 split-K through a
 // global fp32 workspace reduced by the tile's last CTA, 3 persistent stream-K; splits <= 0 picks the default.
 Tensor linear_variant(Tensor x, Tensor w, int64_t mode, int64_t splits) {
@@ -784,6 +811,8 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
         py::arg("x"), py::arg("wq"), py::arg("sw"), py::arg("splits") = 0);
   m.def("topk_logp", &topk_logp, "fused log-softmax + top-k (+ draft-to-target id map)", py::arg("logits"),
         py::arg("k"), py::arg("floor"), py::arg("d2t") = py::none());
+  m.def("linear_sp24", &linear_sp24, "2:4 sparse linear (kept values + positions, expanded in shared memory)",
+        py::arg("x"), py::arg("values"), py::arg("meta"), py::arg("splits") = 0);
   m.def("linear_variant", &linear_variant, "x @ w.T through an explicit GEMM variant (tuning)");
   m.def("gemm_cluster_capacity", &gemm_cluster_capacity, "resident clusters of the split-K cluster GEMM");
   m.def("raise_formatted", &raise_formatted, "raise a formatted RuntimeError (exception-path self test)");

@@ -19,6 +19,10 @@
 //         so the pair (k_2i, k_2i+1) is (word >> 4i) & 0x000F000F. Values are unsigned codes 0..15.
 //   int8  uint8 [N, K]; each word holds 4 consecutive k in the byte order k0 k2 k1 k3, stored as q + 128.
 //   fp8   uint8 [N, K] e4m3 codes in natural order.
+//   sp24  2:4 sparse bf16 weights (no scales): the kept values [N, K / 2] and their positions [N / 2, K / 4] bytes
+//         (per row and 64-wide K-block 8 bytes, 4 bits per group of 4: the two kept positions; rows 2p and 2p + 1
+//         share a 16-byte line). The expansion to dense bf16 happens in shared memory, so a decode pass streams 56 %
+//         of the dense bytes.
 // scales bf16 [K/group, N]; zeros (int4) bf16 [K/group, N] holding 128 + z, so that (128 + q) - (128 + z) = q - z.
 #include <algorithm>
 
@@ -39,16 +43,19 @@ constexpr int kThreads = 192;
 
 template <int FMT>
 struct WqFmt {
+  // int4: 32 B of codes per row and K-block; int8/fp8: 64 B; 2:4 sparse: the 32 kept bf16 values (64 B)
   static constexpr int kRawRowBytes = FMT == kWqInt4 ? kBK / 2 : kBK;
   static constexpr int kRawBytes = kBM * kRawRowBytes;
   static constexpr bool kZeros = FMT == kWqInt4;
+  // per-stage side data: one bf16 scale per row, or the 2:4 positions (8 B per row)
+  static constexpr int kSideBytes = FMT == kWqSp24 ? kBM * 8 : kBM * 2;
 };
 
 template <int FMT, int BN>
 struct WqCfg {
   static constexpr int kOcc = BN <= 64 ? 2 : 1;
   static constexpr int kXBytes = BN * kBK * 2;
-  static constexpr int kLoadBytes = kXBytes + WqFmt<FMT>::kRawBytes + 2 * kBM * 2;  // X + raw + scales + zeros
+  static constexpr int kLoadBytes = kXBytes + WqFmt<FMT>::kRawBytes + WqFmt<FMT>::kSideBytes + kBM * 2;
   static constexpr int kBudget = (kOcc == 1 ? 200 : 100) * 1024;
   static constexpr int kStages = std::min(8, (kBudget - kConvStages * kConvBytes) / kLoadBytes);
   static constexpr int kTmemCols = BN < 32 ? 32 : BN;
@@ -56,7 +63,7 @@ struct WqCfg {
   static constexpr int kXOff = kConvStages * kConvBytes;
   static constexpr int kRawOff = kXOff + kStages * kXBytes;
   static constexpr int kScaleOff = kRawOff + kStages * WqFmt<FMT>::kRawBytes;
-  static constexpr int kZeroOff = kScaleOff + kStages * kBM * 2;
+  static constexpr int kZeroOff = kScaleOff + kStages * WqFmt<FMT>::kSideBytes;
   static constexpr int kBarOff = kZeroOff + kStages * kBM * 2;
   static constexpr int kSmem = kBarOff + 256 + 1024;
   static_assert(BN * kBM * 4 <= kBarOff, "the fp32 partial tile must fit the rings");
@@ -109,6 +116,25 @@ __device__ __forceinline__ uint4 dequant_chunk(const uint32_t* w, int j, __nv_bf
   return make_uint4(out[0], out[1], out[2], out[3]);
 }
 
+// 2:4 sparse: chunk j of a row holds groups 2j and 2j + 1 (4 K-positions each); group g keeps values
+// w[2g], w[2g + 1] at positions (meta >> 4g) & 3 and (meta >> (4g + 2)) & 3, the other two positions are zero.
+__device__ __forceinline__ uint4 expand_sp24(const uint32_t* w, uint64_t meta, int j) {
+  uint32_t out[4];
+#pragma unroll
+  for (int h = 0; h < 2; ++h) {
+    const int g = 2 * j + h;
+    const uint32_t pair = w[g];  // two bf16 values
+    const uint32_t m = static_cast<uint32_t>(meta >> (4 * g)) & 0xFu;
+    const uint32_t i0 = m & 3u, i1 = (m >> 2) & 3u;
+    uint16_t slot[4] = {0, 0, 0, 0};
+    slot[i0] = static_cast<uint16_t>(pair & 0xFFFFu);
+    slot[i1] = static_cast<uint16_t>(pair >> 16);
+    out[2 * h] = slot[0] | (static_cast<uint32_t>(slot[1]) << 16);
+    out[2 * h + 1] = slot[2] | (static_cast<uint32_t>(slot[3]) << 16);
+  }
+  return make_uint4(out[0], out[1], out[2], out[3]);
+}
+
 template <int FMT, int BN>
 __global__ void __launch_bounds__(kThreads, WqCfg<FMT, BN>::kOcc)
     gemm_wq_kernel(const __grid_constant__ CUtensorMap tm_w, const __grid_constant__ CUtensorMap tm_s,
@@ -141,7 +167,7 @@ __global__ void __launch_bounds__(kThreads, WqCfg<FMT, BN>::kOcc)
   const int total_kb = K / kBK;
   const int kb0 = static_cast<int>(blockIdx.z) * kb_per_split;
   const int nkb = max(0, min(kb_per_split, total_kb - kb0));
-  constexpr uint32_t kStageTx = Cfg::kXBytes + F::kRawBytes + kBM * 2 * (F::kZeros ? 2 : 1);
+  constexpr uint32_t kStageTx = Cfg::kXBytes + F::kRawBytes + F::kSideBytes + (F::kZeros ? kBM * 2 : 0);
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < S; ++s) {
@@ -172,6 +198,12 @@ __global__ void __launch_bounds__(kThreads, WqCfg<FMT, BN>::kOcc)
     const int pre = nkb < S ? nkb : S;
     auto load_w = [&](int s, int kb) {
       const int k = (kb0 + kb) * kBK;
+      if constexpr (FMT == kWqSp24) {
+        tma_load_2d(raw + s * F::kRawBytes, &tm_w, &full[s], k / 2, n0);  // bf16 values [N, K / 2]
+        tma_load_2d(reinterpret_cast<uint8_t*>(scales) + s * F::kSideBytes, &tm_s, &full[s], (k / kBK) * 16,
+                    n0 / 2);  // positions [N / 2, K / 4] bytes: a row pair's 16 B per K-block
+        return;
+      }
       tma_load_2d(raw + s * F::kRawBytes, &tm_w, &full[s], k * F::kRawRowBytes / kBK, n0);
       tma_load_2d(scales + s * kBM, &tm_s, &full[s], n0, k / group);
       if (F::kZeros) tma_load_2d(zeros + s * kBM, &tm_z, &full[s], n0, k / group);
@@ -215,7 +247,14 @@ __global__ void __launch_bounds__(kThreads, WqCfg<FMT, BN>::kOcc)
       const int s = kb % S, c = kb % kConvStages;
       if (!mbar_wait(&full[s], (kb / S) & 1u, status, kStatusWaitFull, abort_flag)) break;
       if (!mbar_wait(&conv_empty[c], ((kb / kConvStages) & 1u) ^ 1u, status, kStatusWaitEmpty, abort_flag)) break;
-      const bf16 sc = scales[s * kBM + row];
+      uint64_t meta = 0;
+      bf16 sc = __float2bfloat16(1.f);
+      if constexpr (FMT == kWqSp24) {
+        meta = *reinterpret_cast<const uint64_t*>(reinterpret_cast<const uint8_t*>(scales) + s * F::kSideBytes +
+                                                  (row >> 1) * 16 + (row & 1) * 8);
+      } else {
+        sc = scales[s * kBM + row];
+      }
       const __nv_bfloat162 s2 = __halves2bfloat162(sc, sc);
       __nv_bfloat162 z2 = __halves2bfloat162(__float2bfloat16(0.f), __float2bfloat16(0.f));
       if (F::kZeros) {
@@ -232,7 +271,9 @@ __global__ void __launch_bounds__(kThreads, WqCfg<FMT, BN>::kOcc)
       uint8_t* dst_row = conv + c * kConvBytes + row * 128;
 #pragma unroll
       for (int j = 0; j < 8; ++j) {
-        const uint4 v = dequant_chunk<FMT>(words, j, s2, z2);
+        uint4 v;
+        if constexpr (FMT == kWqSp24) v = expand_sp24(words, meta, j);
+        else v = dequant_chunk<FMT>(words, j, s2, z2);
         *reinterpret_cast<uint4*>(dst_row + ((j ^ (row & 7)) << 4)) = v;
       }
       fence_async_smem();
@@ -369,6 +410,7 @@ int launch_gemm_wq(const WqMaps& maps, void* y, int M, int N, int K, int group, 
     case kWqInt4: return run_wq_bn<kWqInt4>(maps, y, M, N, K, group, splits, status, stream);
     case kWqInt8: return run_wq_bn<kWqInt8>(maps, y, M, N, K, group, splits, status, stream);
     case kWqFp8: return run_wq_bn<kWqFp8>(maps, y, M, N, K, group, splits, status, stream);
+    case kWqSp24: return run_wq_bn<kWqSp24>(maps, y, M, N, K, K, splits, status, stream);
     default: return -1;
   }
 }
