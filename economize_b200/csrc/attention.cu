@@ -114,7 +114,8 @@ __global__ void __launch_bounds__(kThreads, 1)
                    float* __restrict__ ws_ml, const int* __restrict__ kv_len, const int* __restrict__ n_new,
                    const int64_t* __restrict__ mask, int T, int H, int Hkv, int S, float scale_log2, int q_offset,
                    int chunks_per_split, int m_tiles, unsigned* status, unsigned long long* trace,
-                   const float* __restrict__ k_scale, const float* __restrict__ v_scale) {
+                   const float* __restrict__ k_scale, const float* __restrict__ v_scale,
+                   const uint32_t* __restrict__ keep, float* __restrict__ lse_out) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* q_tile = smem;
@@ -259,7 +260,14 @@ __global__ void __launch_bounds__(kThreads, 1)
     float sc[32];
     tmem_ld16(tmem_s + lane_off, sc);
     tmem_ld16(tmem_s + lane_off + 16, sc + 16);
-    const uint32_t vis = visible32(c * kKeys + col0, base, nn, use_mask, bits, causal_lim, row_valid);
+    uint32_t vis = visible32(c * kKeys + col0, base, nn, use_mask, bits, causal_lim, row_valid);
+    if (keep != nullptr) {  // evicted committed slots are invisible (new slots are never evicted)
+      const int s0 = c * kKeys + col0;
+      const uint32_t kw = keep[(static_cast<size_t>(b) * Hkv + kvh) * (S / 32) + s0 / 32];
+      const int pre = min(max(base - s0, 0), 32);
+      const uint32_t committed = pre >= 32 ? 0xffffffffu : ((1u << pre) - 1u);
+      vis &= kw | ~committed;
+    }
     float qmax = -INFINITY;
 #pragma unroll
     for (int j = 0; j < 32; ++j) {
@@ -336,6 +344,8 @@ __global__ void __launch_bounds__(kThreads, 1)
 
   if (!failed && row_valid) {
     if (splits == 1) {
+      if (lse_out != nullptr && quarter == 0)  // log2-domain log-sum-exp of the row's scaled scores
+        lse_out[(static_cast<size_t>(b) * T + t) * H + head] = l_tot > 0.f ? m_run + __log2f(l_tot) : -INFINITY;
       const float inv = l_tot > 0.f ? 1.f / l_tot : 0.f;
       uint4* dst = reinterpret_cast<uint4*>(out + ((static_cast<size_t>(b) * T + t) * H + head) * kDim + col0);
 #pragma unroll
@@ -366,7 +376,8 @@ __global__ void __launch_bounds__(kThreads, 1)
 // Combine the split partials of every packed row: out = sum_s O_s 2^(m_s - M) / sum_s l_s 2^(m_s - M).
 __global__ void __launch_bounds__(128) attn_merge_kernel(const float* __restrict__ ws_o,
                                                          const float* __restrict__ ws_ml, bf16* __restrict__ out,
-                                                         int T, int H, int Hkv, int m_tiles, int splits) {
+                                                         int T, int H, int Hkv, int m_tiles, int splits,
+                                                         float* __restrict__ lse_out) {
   pdl_trigger();
   pdl_wait();
   const int tile = blockIdx.x;  // (b * Hkv + kvh) * m_tiles + m_tile
@@ -396,9 +407,117 @@ __global__ void __launch_bounds__(128) attn_merge_kernel(const float* __restrict
     denom += l * w;
   }
   const float inv = denom > 0.f ? 1.f / denom : 0.f;
+  if (lse_out != nullptr && lane == 0)
+    lse_out[(static_cast<size_t>(b) * T + t) * H + head] = denom > 0.f ? mx + __log2f(denom) : -INFINITY;
   bf16* dst = out + ((static_cast<size_t>(b) * T + t) * H + head) * kDim + lane * 4;
   *reinterpret_cast<__nv_bfloat162*>(dst) = __floats2bfloat162_rn(acc.x * inv, acc.y * inv);
   *reinterpret_cast<__nv_bfloat162*>(dst + 2) = __floats2bfloat162_rn(acc.z * inv, acc.w * inv);
+}
+
+// ---- attention scores for KV eviction (H2O / SnapKV / PyramidKV) -------------------------------------------------
+// scores[b, kvh, s] += sum over the query rows of KV head kvh (the GQA group's heads x the pass's tokens) of the
+// normalised attention probability exp2(S * scale_log2 - lse2[row]), for every visible slot s. One CTA per (packed
+// 128-row tile, 128-key chunk): S = Q K^T on the tensor cores into TMEM, probabilities in registers, column sums
+// through shared memory, one atomic add per key and tile. lse2 comes from a pass of attn_tc_kernel with lse_out.
+constexpr int kScoreSmem = 2 * kTile + kRows * kKeys * 4 + 1024 + 64;
+
+__global__ void __launch_bounds__(kThreads, 1)
+    attn_scores_kernel(const bf16* __restrict__ q, const __grid_constant__ CUtensorMap tm_k,
+                       const float* __restrict__ lse2, float* __restrict__ scores, const int* __restrict__ kv_len,
+                       const int* __restrict__ n_new, const int64_t* __restrict__ mask, int T, int H, int Hkv, int S,
+                       float scale_log2, int q_offset, int m_tiles, unsigned* status) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* q_tile = smem;
+  uint8_t* k_tile = smem + kTile;
+  float* colbuf = reinterpret_cast<float*>(smem + 2 * kTile);  // [128 rows][128 keys]
+  uint64_t* kv_full = reinterpret_cast<uint64_t*>(smem + 2 * kTile + kRows * kKeys * 4);
+  uint64_t* bar_s = kv_full + 1;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bar_s + 1);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+  pdl_trigger();
+  pdl_wait();
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int quad = warp & 3, quarter = warp >> 2;
+  const int r = quad * 32 + lane;
+  const int m_tile = blockIdx.x % m_tiles, bh = blockIdx.x / m_tiles;
+  const int b = bh / Hkv, kvh = bh % Hkv;
+  const int G = H / Hkv;
+  const int p = m_tile * kRows + r;
+  const int t = p / G, head = kvh * G + p % G;
+  const bool row_valid = t < T;
+  const int base = kv_len[b], nn = n_new[b];
+  const int c = blockIdx.y;  // key chunk
+  const int end = base + nn;
+  if (c * kKeys >= end) return;  // uniform: the whole CTA leaves
+  const bool use_mask = mask != nullptr;
+  const uint64_t bits = (row_valid && use_mask) ? static_cast<uint64_t>(mask[static_cast<size_t>(b) * T + t]) : 0ull;
+  const float l2 = row_valid ? lse2[(static_cast<size_t>(b) * T + t) * H + head] : 0.f;
+
+  if (tid == 0) {
+    mbar_init(kv_full, 1);
+    mbar_init(bar_s, 1);
+    *abort_flag = 0;
+    fence_mbar_init();
+    mbar_arrive_expect_tx(kv_full, 2 * kAtom);
+    const int y = static_cast<int>((static_cast<size_t>(b) * Hkv + kvh) * S + static_cast<size_t>(c) * kKeys);
+    tma_load_2d(k_tile, &tm_k, kv_full, 0, y);
+    tma_load_2d(k_tile + kAtom, &tm_k, kv_full, 64, y);
+  }
+  __syncwarp();
+  if (warp == 0) tmem_alloc(tmem_slot, 128);
+  {
+    const uint4* src = reinterpret_cast<const uint4*>(q + (static_cast<size_t>(b) * T + t) * H * kDim +
+                                                      static_cast<size_t>(head) * kDim);
+#pragma unroll
+    for (int u = 0; u < 4; ++u) {
+      const int chunk = quarter * 4 + u;
+      store_row_swizzled(q_tile, r, chunk, row_valid ? src[chunk] : make_uint4(0, 0, 0, 0));
+    }
+  }
+  fence_async_smem();
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+  bool ok = mbar_wait(kv_full, 0, status, kStatusWaitFull, abort_flag);
+  if (ok && tid == 0) {
+    tc_fence_after();
+    constexpr uint32_t idesc = idesc_bf16_f32(kRows, kKeys);
+    const uint32_t qa = smem_u32(q_tile), ka = smem_u32(k_tile);
+#pragma unroll
+    for (int kk = 0; kk < kDim / 16; ++kk) {
+      const uint32_t off = (kk >> 2) * kAtom + (kk & 3) * 32;
+      umma_bf16(tmem, desc_kmajor_sw128(qa + off), desc_kmajor_sw128(ka + off), idesc, kk != 0);
+    }
+    umma_commit(bar_s);
+  }
+  __syncwarp();
+  ok = ok && mbar_wait(bar_s, 0, status, kStatusWaitAccum, abort_flag);
+  __syncthreads();
+  ok = !*abort_flag;
+  tc_fence_after();
+  const uint32_t col0 = quarter * 32;
+  if (ok) {
+    float sc[32];
+    tmem_ld16(tmem + (static_cast<uint32_t>(quad * 32) << 16) + col0, sc);
+    tmem_ld16(tmem + (static_cast<uint32_t>(quad * 32) << 16) + col0 + 16, sc + 16);
+    const uint32_t vis = visible32(c * kKeys + col0, base, nn, use_mask, bits, q_offset + t + 1, row_valid);
+#pragma unroll
+    for (int j = 0; j < 32; ++j)
+      colbuf[r * kKeys + col0 + j] = ((vis >> j) & 1u) ? fast_exp2(sc[j] * scale_log2 - l2) : 0.f;
+  }
+  __syncthreads();
+  if (ok && tid < kKeys) {
+    float acc = 0.f;
+    for (int row = 0; row < kRows; ++row) acc += colbuf[row * kKeys + tid];
+    const int slot = c * kKeys + tid;
+    if (slot < end && acc != 0.f) atomicAdd(scores + (static_cast<size_t>(b) * Hkv + kvh) * S + slot, acc);
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 0) tmem_dealloc(tmem, 128);
 }
 
 }  // namespace
@@ -423,7 +542,8 @@ AttnPlan attention_plan(int B, int T, int H, int Hkv, int S, int num_sms) {
 int launch_attention(const void* q, const CUtensorMap* tm_k, const CUtensorMap* tm_v, void* out, float* ws,
                      const int* kv_len, const int* n_new, const int64_t* mask, int B, int T, int H, int Hkv, int D,
                      int S, float scale, int q_offset, const AttnPlan& plan, unsigned* status, cudaStream_t stream,
-                     unsigned long long* trace, const float* k_scale, const float* v_scale) {
+                     unsigned long long* trace, const float* k_scale, const float* v_scale, const uint32_t* keep,
+                     float* lse_out) {
   if (D != kDim || H % Hkv != 0) return -1;
   if (mask != nullptr && T > 64) return -1;
   const bool fp8 = k_scale != nullptr;
@@ -441,12 +561,30 @@ int launch_attention(const void* q, const CUtensorMap* tm_k, const CUtensorMap* 
   launch_pdl(fp8 ? attn_tc_kernel<true> : attn_tc_kernel<false>, grid, dim3(kThreads), kSmem, stream,
              static_cast<const bf16*>(q), *tm_k, *tm_v, static_cast<bf16*>(out), ws_o, ws_ml, kv_len, n_new, mask, T,
              H, Hkv, S, scale * 1.4426950408889634f, q_offset, plan.chunks_per_split, plan.m_tiles, status, trace,
-             k_scale, v_scale);
+             k_scale, v_scale, keep, lse_out);
   if (plan.splits > 1) {
     dim3 mgrid(ctas, kRows / 4);
     launch_pdl(attn_merge_kernel, mgrid, dim3(128), 0, stream, static_cast<const float*>(ws_o),
-               static_cast<const float*>(ws_ml), static_cast<bf16*>(out), T, H, Hkv, plan.m_tiles, plan.splits);
+               static_cast<const float*>(ws_ml), static_cast<bf16*>(out), T, H, Hkv, plan.m_tiles, plan.splits,
+               lse_out);
   }
+  return 0;
+}
+
+int launch_attention_scores(const void* q, const CUtensorMap* tm_k, const float* lse2, float* scores,
+                            const int* kv_len, const int* n_new, const int64_t* mask, int B, int T, int H, int Hkv,
+                            int D, int S, float scale, int q_offset, unsigned* status, cudaStream_t stream) {
+  if (D != kDim || H % Hkv != 0 || (mask != nullptr && T > 64)) return -1;
+  static bool configured = false;
+  if (!configured) {
+    cudaFuncSetAttribute(attn_scores_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kScoreSmem);
+    configured = true;
+  }
+  const int G = H / Hkv;
+  const int m_tiles = (T * G + kRows - 1) / kRows;
+  dim3 grid(B * Hkv * m_tiles, (S + kKeys - 1) / kKeys);
+  launch_pdl(attn_scores_kernel, grid, dim3(kThreads), kScoreSmem, stream, static_cast<const bf16*>(q), *tm_k, lse2,
+             scores, kv_len, n_new, mask, T, H, Hkv, S, scale * 1.4426950408889634f, q_offset, m_tiles, status);
   return 0;
 }
 

@@ -195,7 +195,7 @@ Tensor rope_store(Tensor qkv, Tensor positions, Tensor cos, Tensor sin, int64_t 
 
 Tensor attention(Tensor q, Tensor k_cache, Tensor v_cache, Tensor kv_len, Tensor n_new, c10::optional<Tensor> mask,
                  double scale, int64_t q_offset, c10::optional<Tensor> trace, c10::optional<Tensor> k_scale,
-                 c10::optional<Tensor> v_scale) {
+                 c10::optional<Tensor> v_scale, c10::optional<Tensor> keep, c10::optional<Tensor> lse_out) {
   CHECK_CUDA(q);
   CHECK_BF16(q);
   TORCH_CHECK(q.dim() == 4 && q.size(3) == 128 && k_cache.dim() == 4, "attention: head_dim must be 128");
@@ -218,6 +218,16 @@ Tensor attention(Tensor q, Tensor k_cache, Tensor v_cache, Tensor kv_len, Tensor
     TORCH_CHECK(T <= 64, "tree masks cover at most 64 new tokens");
     mask_ptr = m.data_ptr<int64_t>();
   }
+  if (keep.has_value()) {
+    CHECK_I32(*keep);
+    TORCH_CHECK(keep->is_contiguous() && keep->numel() == static_cast<int64_t>(B) * Hkv * (S / 32),
+                "keep must be int32 [B, Hkv, S / 32] bit words");
+  }
+  if (lse_out.has_value()) {
+    TORCH_CHECK(lse_out->scalar_type() == at::kFloat && lse_out->is_contiguous() &&
+                    lse_out->numel() == static_cast<int64_t>(B) * T * H,
+                "lse_out must be fp32 [B, T, H]");
+  }
   auto out = at::empty_like(q);
   const ecz::AttnPlan plan = ecz::attention_plan(B, T, H, Hkv, S, num_sms(q.get_device()));
   Tensor ws;
@@ -236,7 +246,10 @@ Tensor attention(Tensor q, Tensor k_cache, Tensor v_cache, Tensor kv_len, Tensor
                                                                trace->data_ptr<int64_t>())
                                                          : nullptr,
                                        fp8 ? k_scale->data_ptr<float>() : nullptr,
-                                       fp8 ? v_scale->data_ptr<float>() : nullptr);
+                                       fp8 ? v_scale->data_ptr<float>() : nullptr,
+                                       keep.has_value() ? reinterpret_cast<const uint32_t*>(keep->data_ptr<int>())
+                                                        : nullptr,
+                                       lse_out.has_value() ? lse_out->data_ptr<float>() : nullptr);
   TORCH_CHECK(rc == 0, "attention: unsupported shape (head_dim must be 128, H divisible by H_kv)");
   return out;
 }
@@ -511,6 +524,35 @@ Tensor linear_sp24(Tensor x, Tensor values, Tensor meta, int64_t splits) {
                                      at::cuda::getCurrentCUDAStream());
   TORCH_CHECK(rc == 0, "linear_sp24: launch failed (", rc, ")");
   return y;
+}
+
+// Accumulate KV-eviction scores [B, Hkv, S] (fp32, in place) for the queries q [B, T, H, D] of a pass whose
+// log2-domain log-sum-exp lse2 [B, T, H] came from attention(..., lse_out=).
+void attention_scores(Tensor q, Tensor k_cache, Tensor kv_len, Tensor n_new, c10::optional<Tensor> mask,
+                      Tensor lse2, Tensor scores, double scale, int64_t q_offset) {
+  CHECK_CUDA(q);
+  CHECK_BF16(q);
+  CHECK_BF16(k_cache);
+  TORCH_CHECK(q.dim() == 4 && q.size(3) == 128 && k_cache.dim() == 4, "attention_scores: head_dim must be 128");
+  c10::cuda::CUDAGuard guard(q.device());
+  q = q.contiguous();
+  const int B = static_cast<int>(q.size(0)), T = static_cast<int>(q.size(1)), H = static_cast<int>(q.size(2));
+  const int Hkv = static_cast<int>(k_cache.size(1)), S = static_cast<int>(k_cache.size(2));
+  TORCH_CHECK(scores.scalar_type() == at::kFloat && scores.is_contiguous() &&
+                  scores.numel() == static_cast<int64_t>(B) * Hkv * S, "scores must be fp32 [B, Hkv, S]");
+  TORCH_CHECK(lse2.scalar_type() == at::kFloat && lse2.numel() == static_cast<int64_t>(B) * T * H, "lse2 [B, T, H]");
+  Tensor m;
+  if (mask.has_value()) {
+    m = mask->contiguous();
+    CHECK_I64(m);
+  }
+  const CUtensorMap* tk = tensor_map(k_cache.data_ptr(), static_cast<uint64_t>(B) * Hkv * S, 128, 128, 128);
+  const int rc = ecz::launch_attention_scores(q.data_ptr(), tk, lse2.contiguous().data_ptr<float>(),
+                                              scores.data_ptr<float>(), kv_len.data_ptr<int>(), n_new.data_ptr<int>(),
+                                              mask.has_value() ? m.data_ptr<int64_t>() : nullptr, B, T, H, Hkv, 128, S,
+                                              static_cast<float>(scale), static_cast<int>(q_offset),
+                                              status_word(q.device()), at::cuda::getCurrentCUDAStream());
+  TORCH_CHECK(rc == 0, "attention_scores: unsupported shape");
 }
 
 // Explicit GEMM variant (tuning and benchmarks): mode 1 cluster split-K (DSMEM reduction), 2 split-K through a
@@ -800,7 +842,8 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("attention", &attention, "tree-masked / causal attention over the slot cache (tcgen05; bf16 or fp8 KV)",
         py::arg("q"), py::arg("k_cache"), py::arg("v_cache"), py::arg("kv_len"), py::arg("n_new"), py::arg("mask"),
         py::arg("scale"), py::arg("q_offset"), py::arg("trace") = py::none(), py::arg("k_scale") = py::none(),
-        py::arg("v_scale") = py::none());
+        py::arg("v_scale") = py::none(), py::arg("keep") = py::none(), py::arg("lse_out") = py::none());
+  m.def("attention_scores", &attention_scores, "accumulate KV-eviction attention scores (tcgen05)");
   m.def("silu_mul", &silu_mul, "SwiGLU activation of [gate; up]");
   m.def("linear_parts", &linear_parts, "x @ w.T as bf16 or fp32 split-K partials for a fusing consumer");
   m.def("moe_route", &moe_route, "top-k expert routing with deterministic expert-order positions");

@@ -78,7 +78,11 @@ int launch_attention(const void* q, const CUtensorMap* tm_k, const CUtensorMap* 
                      const int* kv_len, const int* n_new, const int64_t* mask, int B, int T, int H, int Hkv, int D,
                      int S, float scale, int q_offset, const AttnPlan& plan, unsigned* status, cudaStream_t stream,
                      unsigned long long* trace = nullptr, const float* k_scale = nullptr,
-                     const float* v_scale = nullptr);
+                     const float* v_scale = nullptr, const uint32_t* keep = nullptr, float* lse_out = nullptr);
+// KV-eviction scores: scores[b, kvh, s] += attention probability mass of slot s (see attention.cu)
+int launch_attention_scores(const void* q, const CUtensorMap* tm_k, const float* lse2, float* scores,
+                            const int* kv_len, const int* n_new, const int64_t* mask, int B, int T, int H, int Hkv,
+                            int D, int S, float scale, int q_offset, unsigned* status, cudaStream_t stream);
 
 // sampling.cu
 int launch_topk_logp(const float* logits, const int64_t* d2t, float* vals, int64_t* ids, int rows, int V, int k,

@@ -79,6 +79,8 @@ class CausalLM(nn.Module):
         self.observer = None
         #: KV-cache storage set by KV techniques: dtype (None: the compute dtype) and fp8 scales ([L, H_kv] x 2)
         self.kv_dtype: torch.dtype | None = None
+        #: KV eviction policy (a kv_evict technique): scores the prompt at prefill, hides evicted slots afterwards
+        self.kv_evictor = None
         self.kv_scales: tuple[torch.Tensor, torch.Tensor] | None = None
         #: tensor-parallel group (set by economize_b200.parallel.tp.shard_model) and this rank's shard sizes
         self.tp = None
@@ -186,8 +188,11 @@ class CausalLM(nn.Module):
                            c.head_dim, k_cache,
                            v_cache, batch.kv_len, batch.n_new, layer.q_norm, layer.k_norm, c.rms_norm_eps,
                            q_offset=batch.q_offset, k_scale=k_scale, v_scale=v_scale)
+        keep = self.kv_evictor.keep_for(index, k_cache) if self.kv_evictor is not None else None
         o = ops.attention(q, k_cache, v_cache, batch.kv_len, batch.n_new, batch.mask, q_offset=batch.q_offset,
-                          k_scale=k_scale, v_scale=v_scale)
+                          k_scale=k_scale, v_scale=v_scale, keep=keep)
+        if self.kv_evictor is not None and batch.is_prefill:
+            self.kv_evictor.observe_prefill(index, q, k_cache, v_cache, batch)
         o = o.reshape(*o.shape[:2], -1)
         if self.observer is not None:
             self.observer(index, "wo", o)

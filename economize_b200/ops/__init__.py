@@ -18,6 +18,7 @@ from .sparse import Sparse24Weight
 __all__ = [
     "argmax",
     "attention",
+    "attention_scores",
     "available",
     "greedy_accept",
     "kv_compact",
@@ -119,15 +120,28 @@ def rope_store(qkv: torch.Tensor, positions: torch.Tensor, cos: torch.Tensor, si
 def attention(q: torch.Tensor, k_cache: torch.Tensor, v_cache: torch.Tensor, kv_len: torch.Tensor,
               n_new: torch.Tensor, mask: torch.Tensor | None = None, scale: float | None = None,
               q_offset: int = 0, k_scale: torch.Tensor | None = None,
-              v_scale: torch.Tensor | None = None) -> torch.Tensor:
+              v_scale: torch.Tensor | None = None, keep: torch.Tensor | None = None,
+              lse_out: torch.Tensor | None = None) -> torch.Tensor:
     """Causal / tree-masked attention over the slot cache (see :func:`.reference.attention`); fp8 caches take
-    per-KV-head scales."""
+    per-KV-head scales, ``keep`` (int32 bit words ``[B, H_kv, S / 32]``) hides evicted committed slots and
+    ``lse_out [B, T, H]`` receives every row's log2-domain log-sum-exp."""
     scale = float(scale if scale is not None else q.shape[-1] ** -0.5)
     if q.is_cuda:
         return require().attention(q, k_cache, v_cache, kv_len, n_new, mask, scale, int(q_offset), None, k_scale,
-                                   v_scale)
+                                   v_scale, keep, lse_out)
     return reference.attention(q, k_cache, v_cache, kv_len, n_new, mask, scale, q_offset=q_offset, k_scale=k_scale,
-                               v_scale=v_scale)
+                               v_scale=v_scale, keep=keep, lse_out=lse_out)
+
+
+def attention_scores(q: torch.Tensor, k_cache: torch.Tensor, kv_len: torch.Tensor, n_new: torch.Tensor,
+                     mask: torch.Tensor | None, lse2: torch.Tensor, scores: torch.Tensor,
+                     scale: float | None = None, q_offset: int = 0) -> None:
+    """Accumulate KV-eviction scores (H2O / SnapKV) into ``scores [B, H_kv, S]`` on the tensor cores."""
+    scale = float(scale if scale is not None else q.shape[-1] ** -0.5)
+    if q.is_cuda:
+        require().attention_scores(q, k_cache, kv_len, n_new, mask, lse2, scores, scale, int(q_offset))
+        return
+    reference.attention_scores(q, k_cache, kv_len, n_new, mask, lse2, scores, scale, q_offset)
 
 
 def silu_mul(gate_up: torch.Tensor | Partials) -> torch.Tensor:

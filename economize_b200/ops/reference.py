@@ -97,7 +97,8 @@ def visible_mask(kv_len: torch.Tensor, n_new: torch.Tensor, length: int, width: 
 def attention(q: torch.Tensor, k_cache: torch.Tensor, v_cache: torch.Tensor, kv_len: torch.Tensor,
               n_new: torch.Tensor, mask: torch.Tensor | None = None, scale: float | None = None,
               softcap: float | None = None, q_offset: int = 0, k_scale: torch.Tensor | None = None,
-              v_scale: torch.Tensor | None = None) -> torch.Tensor:
+              v_scale: torch.Tensor | None = None, keep: torch.Tensor | None = None,
+              lse_out: torch.Tensor | None = None) -> torch.Tensor:
     """Attention of queries ``[B, T, H, D]`` over the slot cache ``[B, H_kv, S, D]`` (bf16, fp32, or e4m3 codes with
     per-KV-head scales ``k_scale``/``v_scale``).
 
@@ -120,7 +121,16 @@ def attention(q: torch.Tensor, k_cache: torch.Tensor, v_cache: torch.Tensor, kv_
     scores = torch.matmul(q.float().transpose(1, 2), keys.transpose(-1, -2)) * (scale or dim ** -0.5)
     if softcap is not None:
         scores = torch.tanh(scores / softcap) * softcap
-    scores = scores.masked_fill(~vis[:, None], float("-inf"))
+    vis = vis[:, None].expand(batch, heads, length, width)
+    if keep is not None:  # evicted committed slots (bit words [B, H_kv, S / 32]) are invisible
+        bits = ((keep.long()[..., None] >> torch.arange(32, device=keep.device)) & 1).bool()
+        kept = bits.reshape(batch, kv_heads, -1)[..., :width].repeat_interleave(group, 1)  # [B, H, W]
+        committed = torch.arange(width, device=keep.device)[None, :] < kv_len.long()[:, None]  # [B, W]
+        vis = vis & (kept | ~committed[:, None])[:, :, None, :]
+    scores = scores.masked_fill(~vis, float("-inf"))
+    if lse_out is not None:  # log2-domain log-sum-exp per (row, token, head), like the kernel's
+        lse = torch.logsumexp(scores, -1) * 1.4426950408889634  # [B, H, T]
+        lse_out.copy_(lse.transpose(1, 2))
     probs = torch.softmax(scores, -1).nan_to_num(0.0)
     out = torch.matmul(probs, values).transpose(1, 2)
     return out.to(q.dtype)
@@ -266,3 +276,18 @@ def ngram(history: torch.Tensor, length: torch.Tensor, k: int, min_n: int, max_n
                         out[b, j] = h[i + n + j]
                 break
     return out
+
+
+def attention_scores(q: torch.Tensor, k_cache: torch.Tensor, kv_len: torch.Tensor, n_new: torch.Tensor,
+                     mask: torch.Tensor | None, lse2: torch.Tensor, scores: torch.Tensor, scale: float,
+                     q_offset: int = 0) -> None:
+    """``scores [B, H_kv, S] +=`` the attention probability mass every visible slot receives from the queries
+    ``q [B, T, H, D]`` (probabilities ``exp2(s * scale * log2 e - lse2)``), summed over each KV head's group."""
+    batch, length, heads, dim = q.shape
+    kv_heads, width = k_cache.shape[1], scores.shape[-1]
+    group = heads // kv_heads
+    vis = visible_mask(kv_len, n_new, length, width, mask, q_offset)
+    keys = k_cache[:, :, :width].float().repeat_interleave(group, 1)
+    s = torch.matmul(q.float().transpose(1, 2), keys.transpose(-1, -2)) * scale * 1.4426950408889634
+    p = torch.exp2(s - lse2.float().transpose(1, 2)[..., None]).masked_fill(~vis[:, None], 0.0)
+    scores += p.sum(2).reshape(batch, kv_heads, group, width).sum(2)

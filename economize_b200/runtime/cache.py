@@ -74,6 +74,8 @@ class StepBatch:
     positions: torch.Tensor
     mask: torch.Tensor | None = None
     q_offset: int = 0
+    #: a prompt pass starting at slot 0 (KV eviction scores the prompt during it)
+    is_prefill: bool = False
 
     @staticmethod
     def prefill(lengths: torch.Tensor, width: int) -> StepBatch:
@@ -81,4 +83,5 @@ class StepBatch:
         batch = lengths.shape[0]
         device = lengths.device
         positions = torch.arange(width, device=device, dtype=torch.int32).expand(batch, width).contiguous()
-        return StepBatch(torch.zeros(batch, dtype=torch.int32, device=device), lengths.to(torch.int32), positions)
+        return StepBatch(torch.zeros(batch, dtype=torch.int32, device=device), lengths.to(torch.int32), positions,
+                         is_prefill=True)
