@@ -86,7 +86,7 @@ def _raw(x):
 def linear_parts(x: torch.Tensor, weight) -> torch.Tensor | Partials:
     """``x @ weight.T`` for a consumer that fuses the split-K reduction (:func:`rmsnorm`, :func:`silu_mul`,
     :func:`rope_store`): :class:`Partials` on CUDA when the GEMM splits K, else the plain result."""
-    if not x.is_cuda or isinstance(weight, (QWeight, FP8BlockWeight, Sparse24Weight)) or x.dtype != torch.bfloat16:
+    if not x.is_cuda or not isinstance(weight, torch.Tensor) or x.dtype != torch.bfloat16:
         return linear(x, weight)
     shape = x.shape
     y = require().linear_parts(x.reshape(-1, shape[-1]), weight)
@@ -153,7 +153,7 @@ def silu_mul(gate_up: torch.Tensor | Partials) -> torch.Tensor:
 def linear(x: torch.Tensor, weight, bias: torch.Tensor | None = None) -> torch.Tensor:
     """``x @ weight.T (+ bias)``; on CUDA the tcgen05/TMA GEMM of ``csrc/gemm_tc.cu``, or for a quantized
     :class:`~economize_b200.ops.quant.QWeight` the weight-only GEMM of ``csrc/gemm_wq.cu``."""
-    if isinstance(weight, (QWeight, FP8BlockWeight, Sparse24Weight)):
+    if isinstance(weight, (QWeight, FP8BlockWeight, Sparse24Weight)) or hasattr(weight, "linear"):
         y = weight.linear(x)
         return y if bias is None else y + bias
     if x.is_cuda:

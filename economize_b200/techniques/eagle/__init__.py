@@ -118,7 +118,7 @@ class EagleDrafter:
         x = ops.linear(torch.cat([emb, features.to(t.fc.dtype)], -1), t.fc, t.fc_bias)
         mlp, a = t.layer.run(x, x, self.cache, batch)
         model = t.model
-        normed, out = ops.rmsnorm(mlp, model.norm.to(mlp.dtype), model.config.rms_norm_eps, a)
+        normed, out = ops.rmsnorm(mlp, model.norm.to(a.dtype), model.config.rms_norm_eps, a)
         return ops.linear(normed, model.head_weight).float(), out
 
     def observe(self, tokens, sources, kv_len, n_valid, root):

@@ -243,3 +243,113 @@ class KangarooDistill(Objective):
         with torch.no_grad():
             acc = (logits.argmax(-1) == labels).float().mean()
         return loss, {"loss": float(loss.detach()), "acc": float(acc)}
+
+
+# ---- distillation objectives for EAGLE-3 heads -----------------------------------------------------------------
+DIVERGENCES = ("kl", "rkl", "js", "tvd", "ce_top1")
+
+
+def divergence(student_logp: torch.Tensor, teacher_p: torch.Tensor, kind: str) -> torch.Tensor:
+    """Per-row divergence between a teacher distribution ``teacher_p`` and a student ``exp(student_logp)``."""
+    sp = student_logp.exp()
+    tlog = torch.log(teacher_p.clamp_min(1e-12))
+    if kind == "kl":
+        return (teacher_p * (tlog - student_logp)).sum(-1)
+    if kind == "rkl":
+        return (sp * (student_logp - tlog)).sum(-1)
+    if kind == "js":
+        m = 0.5 * (sp + teacher_p)
+        logm = torch.log(m.clamp_min(1e-12))
+        return 0.5 * (teacher_p * (tlog - logm)).sum(-1) + 0.5 * (sp * (student_logp - logm)).sum(-1)
+    if kind == "tvd":
+        return 0.5 * (sp - teacher_p).abs().sum(-1)
+    if kind == "ce_top1":
+        return -student_logp.gather(-1, teacher_p.argmax(-1, keepdim=True))[..., 0]
+    raise ConfigError(f"unknown divergence {kind!r}; choose from {DIVERGENCES}")
+
+
+def _teacher_draft_probs(model, tech, tokens: torch.Tensor, top_k: int | None):
+    """Teacher next-token probabilities over the EAGLE-3 draft vocabulary ``[B, S, V_d]`` (restricted to the
+    teacher's ``top_k`` tokens when given), plus the captured block outputs."""
+    target = model.model
+    batch, length = tokens.shape
+    cache = target.new_cache(batch, ((length + 127) // 128) * 128)
+    lengths = torch.full((batch,), length, dtype=torch.int32, device=tokens.device)
+    with torch.no_grad():
+        hidden, aux = target.forward_step(tokens, StepBatch.prefill(lengths, length), cache, tech.aux_layers)
+        logits = target.logits(hidden).float()
+        ids = torch.arange(tech.d2t.numel(), device=tokens.device) + tech.d2t
+        drafted = logits[..., ids]  # the draft vocabulary's logits, draft order
+        if top_k is not None:
+            kth = logits.topk(top_k, -1).values[..., -1:]
+            drafted = drafted.masked_fill(drafted < kth, float("-inf"))
+        probs = torch.softmax(drafted, -1).nan_to_num(0.0)
+    return {k: v.detach() for k, v in aux.items()}, probs
+
+
+@OBJECTIVES.register("distill_kl")
+class Eagle3Distill(Objective):
+    """Unrolled EAGLE-3 steps trained against the target's full next-token distribution (restricted to the draft
+    vocabulary) under a divergence (``kl``, ``rkl``, ``js``, ``tvd``, ``ce_top1``)."""
+
+    name = "distill_kl"
+    defaults = OptimDefaults(lr=1e-3, warmup_steps=10)
+
+    def __init__(self, model, divergence: str = "kl", steps: int | None = None, decay: float = 0.8,
+                 top_k: int | None = None) -> None:
+        super().__init__(model)
+        if "eagle3" not in model.techniques:
+            raise ConfigError(f"{self.name} needs an attached eagle3 technique")
+        if divergence not in DIVERGENCES:
+            raise ConfigError(f"unknown divergence {divergence!r}")
+        self.tech = model.techniques["eagle3"]
+        self.kind, self.decay, self.top_k = divergence, decay, top_k
+        self.steps = steps or self.tech.config.train_steps
+
+    def parameters(self) -> list[torch.nn.Parameter]:
+        return [p for p in self.tech.parameters() if p.requires_grad]
+
+    def loss(self, tokens: torch.Tensor) -> tuple[torch.Tensor, dict[str, float]]:
+        from ..techniques.eagle3.train import unrolled_logits
+
+        aux, probs = _teacher_draft_probs(self.model, self.tech, tokens, self.top_k)
+        outs = unrolled_logits(self.tech, aux, tokens, self.steps)
+        positions = torch.arange(tokens.shape[1], device=tokens.device)
+        total, weight, metrics = 0.0, 0.0, {}
+        for j, logits in enumerate(outs, start=1):
+            valid = (positions >= j)[None].expand(tokens.shape[0], -1)
+            d = divergence(torch.log_softmax(logits.float(), -1), probs, self.kind)
+            term = (d * valid).sum() / valid.sum().clamp_min(1)
+            w = self.decay ** (j - 1)
+            total, weight = total + w * term, weight + w
+            metrics[f"div{j}"] = float(term.detach())
+        loss = total / weight
+        metrics["loss"] = float(loss.detach())
+        return loss, metrics
+
+
+@OBJECTIVES.register("hass")
+class HASS(Objective):
+    """HASS (Zhang et al., 2024, "Learning Harmonized Representations for Speculative Sampling"): EAGLE-3's
+    training-time-test cross-entropy plus ``alpha`` times a KL distillation restricted to the target's top-K tokens
+    (harmonized objective distillation), both over the unrolled steps that feed the head its own features
+    (harmonized context alignment). Economize: ``techniques/hass``."""
+
+    name = "hass"
+    defaults = OptimDefaults(lr=1e-3, warmup_steps=10)
+
+    def __init__(self, model, top_k: int = 10, alpha: float = 1.0, steps: int | None = None) -> None:
+        super().__init__(model)
+        self.ttt = Eagle3TTT(model, steps)
+        self.distill = Eagle3Distill(model, "kl", steps, top_k=top_k)
+        self.alpha = alpha
+
+    def parameters(self) -> list[torch.nn.Parameter]:
+        return self.ttt.parameters()
+
+    def loss(self, tokens: torch.Tensor) -> tuple[torch.Tensor, dict[str, float]]:
+        ce, m1 = self.ttt.loss(tokens)
+        kl, m2 = self.distill.loss(tokens)
+        loss = ce + self.alpha * kl
+        return loss, {**{f"ttt_{k}": v for k, v in m1.items()}, **{f"topk_{k}": v for k, v in m2.items()},
+                      "loss": float(loss.detach())}
