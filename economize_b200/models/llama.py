@@ -188,7 +188,7 @@ class CausalLM(nn.Module):
                            c.head_dim, k_cache,
                            v_cache, batch.kv_len, batch.n_new, layer.q_norm, layer.k_norm, c.rms_norm_eps,
                            q_offset=batch.q_offset, k_scale=k_scale, v_scale=v_scale)
-        keep = self.kv_evictor.keep_for(index, k_cache) if self.kv_evictor is not None else None
+        keep = self.kv_evictor.keep_for(index, k_cache, q, batch) if self.kv_evictor is not None else None
         o = ops.attention(q, k_cache, v_cache, batch.kv_len, batch.n_new, batch.mask, q_offset=batch.q_offset,
                           k_scale=k_scale, v_scale=v_scale, keep=keep)
         if self.kv_evictor is not None and batch.is_prefill:

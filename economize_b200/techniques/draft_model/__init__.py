@@ -106,6 +106,7 @@ class DraftLMDrafter:
             self.cache = self.draft.new_cache(batch, capacity)
         else:
             self.cache.reset()
+        self._prompt_pass = True  # the first observe covers the prompt (KV policies of the draft score it)
 
     def fuse(self, aux: dict[int, torch.Tensor]) -> torch.Tensor:
         states = aux[-1]
@@ -116,8 +117,9 @@ class DraftLMDrafter:
         batch, width = tokens.shape
         dev = tokens.device
         pos = (kv_len[:, None] + torch.arange(width, device=dev, dtype=torch.int32)[None]).to(torch.int32)
-        hidden, _ = self.draft.forward_step(tokens, StepBatch(kv_len, n_valid.to(torch.int32), pos.contiguous()),
-                                            self.cache)
+        first, self._prompt_pass = getattr(self, "_prompt_pass", False), False
+        hidden, _ = self.draft.forward_step(tokens, StepBatch(kv_len, n_valid.to(torch.int32), pos.contiguous(),
+                                                              is_prefill=first), self.cache)
         rows = torch.arange(batch, device=dev)
         logits = self.draft.logits(hidden[rows, root.long()]).float()
         return logits, torch.zeros(batch, self.target_hidden, dtype=self.draft.dtype, device=dev)

@@ -93,7 +93,7 @@ class KVEvictTechnique(Technique):
         low = top / cfg.pyramid_ratio
         return max(cfg.window, int(round(top - (top - low) * layer / max(n - 1, 1))))
 
-    def keep_for(self, layer: int, k_cache: torch.Tensor) -> torch.Tensor | None:
+    def keep_for(self, layer: int, k_cache: torch.Tensor, q=None, batch=None) -> torch.Tensor | None:
         if self.keep is None or self.keep.shape[1] != k_cache.shape[0] or self.keep.shape[3] * 32 != k_cache.shape[2]:
             return None
         return self.keep[layer]
