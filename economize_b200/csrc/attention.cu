@@ -75,6 +75,61 @@ __device__ __forceinline__ void convert_fp8_tile(const uint8_t* raw, uint8_t* ti
 }
 
 
+// ---- KIVI (2- or 4-bit) chunks ------------------------------------------------------------------------------------
+// A quantized 128-key chunk of one (layer, row, KV head) is stored contiguously (kivi_chunk_bytes): key codes
+// (token-major, 128 channels x bits), per-channel key scales and zeros (bf16, group = the chunk's 128 tokens), value
+// codes (token-major), per-token value scales and zeros for groups of 32 channels. Dequantisation is
+// bf16(code * scale + zero) with the product and the sum rounded separately in fp32.
+__host__ __device__ constexpr int kivi_code_bytes(int bits) { return kKeys * kDim * bits / 8; }
+__host__ __device__ constexpr int kivi_chunk_bytes(int bits) {
+  return 2 * kivi_code_bytes(bits) + 2 * kDim * 2 + 2 * kKeys * (kDim / 32) * 2;
+}
+
+// Thread tid of 512 fills row tid / 4, channels [32 (tid % 4), + 32) of the K and V tiles of a quantized chunk.
+__device__ __forceinline__ void dequant_kivi_tile(const uint8_t* chunk, int bits, uint8_t* k_tile, uint8_t* v_tile,
+                                                  int tid) {
+  const int row = tid >> 2, part = tid & 3;
+  const int code_row = kDim * bits / 8;  // bytes per token
+  const uint8_t* kc = chunk;
+  const bf16* ks = reinterpret_cast<const bf16*>(chunk + kivi_code_bytes(bits));
+  const bf16* kz = ks + kDim;
+  const uint8_t* vc = chunk + kivi_code_bytes(bits) + 2 * kDim * 2;
+  const bf16* vs = reinterpret_cast<const bf16*>(vc + kivi_code_bytes(bits));
+  const bf16* vz = vs + kKeys * (kDim / 32);
+  const float vscale = __bfloat162float(vs[row * 4 + part]), vzero = __bfloat162float(vz[row * 4 + part]);
+  const int mask = (1 << bits) - 1;
+#pragma unroll
+  for (int u = 0; u < 4; ++u) {  // 8 channels per 16-byte chunk of the swizzled tile
+    const int ch0 = part * 32 + u * 8;
+    uint32_t kw, vw;  // the 8 codes of channels ch0 .. ch0 + 7
+    if (bits == 2) {
+      kw = *reinterpret_cast<const uint16_t*>(kc + row * code_row + ch0 / 4);
+      vw = *reinterpret_cast<const uint16_t*>(vc + row * code_row + ch0 / 4);
+    } else {
+      kw = *reinterpret_cast<const uint32_t*>(kc + row * code_row + ch0 / 2);
+      vw = *reinterpret_cast<const uint32_t*>(vc + row * code_row + ch0 / 2);
+    }
+    uint32_t ko[4], vo[4];
+#pragma unroll
+    for (int e = 0; e < 8; e += 2) {
+      float kv[2], vv[2];
+#pragma unroll
+      for (int h = 0; h < 2; ++h) {
+        const int ch = ch0 + e + h;
+        const float kcode = static_cast<float>((kw >> ((e + h) * bits)) & mask);
+        const float vcode = static_cast<float>((vw >> ((e + h) * bits)) & mask);
+        kv[h] = __fadd_rn(__fmul_rn(kcode, __bfloat162float(ks[ch])), __bfloat162float(kz[ch]));
+        vv[h] = __fadd_rn(__fmul_rn(vcode, vscale), vzero);
+      }
+      __nv_bfloat162 k2 = __floats2bfloat162_rn(kv[0], kv[1]), v2 = __floats2bfloat162_rn(vv[0], vv[1]);
+      ko[e / 2] = *reinterpret_cast<uint32_t*>(&k2);
+      vo[e / 2] = *reinterpret_cast<uint32_t*>(&v2);
+    }
+    store_row_swizzled(k_tile, row, part * 4 + u, make_uint4(ko[0], ko[1], ko[2], ko[3]));
+    store_row_swizzled(v_tile, row, part * 4 + u, make_uint4(vo[0], vo[1], vo[2], vo[3]));
+  }
+}
+
 // Visibility of the 32 slots [s0, s0 + 32) for one query row, bit i = slot s0 + i.
 __device__ __forceinline__ uint32_t visible32(int s0, int base, int nn, bool use_mask, uint64_t bits, int causal_lim,
                                               bool row_valid) {
@@ -115,7 +170,8 @@ __global__ void __launch_bounds__(kThreads, 1)
                    const int64_t* __restrict__ mask, int T, int H, int Hkv, int S, float scale_log2, int q_offset,
                    int chunks_per_split, int m_tiles, unsigned* status, unsigned long long* trace,
                    const float* __restrict__ k_scale, const float* __restrict__ v_scale,
-                   const uint32_t* __restrict__ keep, float* __restrict__ lse_out) {
+                   const uint32_t* __restrict__ keep, float* __restrict__ lse_out,
+                   const uint8_t* __restrict__ kivi, const int* __restrict__ kivi_chunks, int kivi_bits) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* q_tile = smem;
@@ -164,8 +220,13 @@ __global__ void __launch_bounds__(kThreads, 1)
   const int c1 = min(n_chunks, c0 + chunks_per_split);
 
   const size_t kv_row0 = (static_cast<size_t>(b) * Hkv + kvh) * S;
+  const int q_chunks = (!FP8 && kivi != nullptr) ? kivi_chunks[b] : 0;  // chunks [0, q_chunks) are KIVI-coded
   auto issue_kv = [&](int c, int s) {
     const int y = static_cast<int>(kv_row0 + static_cast<size_t>(c) * kKeys);
+    if (c < q_chunks) {  // filled by the threads at its turn; the stage barrier completes without bytes
+      mbar_arrive(&kv_full[s]);
+      return;
+    }
     if constexpr (FP8) {
       mbar_arrive_expect_tx(&kv_full[s], 2 * kRawTile);
       tma_load_2d(raw + s * 2 * kRawTile, &tm_k, &kv_full[s], 0, y);
@@ -234,6 +295,15 @@ __global__ void __launch_bounds__(kThreads, 1)
       fence_async_smem();
       tc_fence_before();
       __syncthreads();
+    } else {
+      if (c < q_chunks) {  // stage s was last read by chunk c - 2, whose MMAs have completed
+        const size_t chunk_id = (static_cast<size_t>(b) * Hkv + kvh) * (S / kKeys) + c;
+        dequant_kivi_tile(kivi + chunk_id * kivi_chunk_bytes(kivi_bits), kivi_bits, k_tiles + s * kTile,
+                          v_tiles + s * kTile, tid);
+        fence_async_smem();
+        tc_fence_before();
+        __syncthreads();
+      }
     }
     if (tid == 0) {
       tc_fence_after();
@@ -520,6 +590,94 @@ __global__ void __launch_bounds__(kThreads, 1)
   if (warp == 0) tmem_dealloc(tmem, 128);
 }
 
+// ---- KIVI quantisation of committed chunks ------------------------------------------------------------------------
+// CTA (layer, row * H_kv + head, i) quantises chunk qc = chunks[row] + i of the bf16 cache when it lies at least
+// `residual` slots behind the row's committed length (its tokens can no longer move). 128 threads: thread d owns
+// key channel d (per-channel scales over the chunk's tokens), then thread t owns token t (per-token value scales).
+__global__ void __launch_bounds__(128) kivi_quantize_kernel(const bf16* __restrict__ cache, uint8_t* __restrict__ kivi,
+                                                            const int* __restrict__ kv_len,
+                                                            const int* __restrict__ chunks, int B, int Hkv, int S,
+                                                            int bits, int residual) {
+  pdl_trigger();
+  pdl_wait();
+  const int layer = blockIdx.x, bh = blockIdx.y, b = bh / Hkv;
+  const int c = chunks[b] + static_cast<int>(blockIdx.z);
+  if ((c + 1) * kKeys + residual > kv_len[b]) return;
+  __shared__ uint8_t codes[kKeys][kDim + 4];
+  const int tid = threadIdx.x;
+  const float levels = static_cast<float>((1 << bits) - 1);
+  const size_t plane = static_cast<size_t>(B) * Hkv * S * kDim;  // one of K / V of one layer
+  const bf16* K = cache + (static_cast<size_t>(layer) * 2) * plane + (static_cast<size_t>(bh) * S + c * kKeys) * kDim;
+  const bf16* V = K + plane;
+  uint8_t* out = kivi + ((static_cast<size_t>(layer) * B * Hkv + bh) * (S / kKeys) + c) * kivi_chunk_bytes(bits);
+  bf16* ks = reinterpret_cast<bf16*>(out + kivi_code_bytes(bits));
+  bf16* kz = ks + kDim;
+  uint8_t* vc = out + kivi_code_bytes(bits) + 2 * kDim * 2;
+  bf16* vs = reinterpret_cast<bf16*>(vc + kivi_code_bytes(bits));
+  bf16* vz = vs + kKeys * (kDim / 32);
+  // keys: channel tid over the chunk's 128 tokens
+  {
+    float lo = INFINITY, hi = -INFINITY;
+    for (int t = 0; t < kKeys; ++t) {
+      const float x = __bfloat162float(K[t * kDim + tid]);
+      lo = fminf(lo, x);
+      hi = fmaxf(hi, x);
+    }
+    const bf16 sb = __float2bfloat16((hi - lo) / levels), zb = __float2bfloat16(lo);
+    const float sc = __bfloat162float(sb) > 0.f ? __bfloat162float(sb) : 1.f, z = __bfloat162float(zb);
+    ks[tid] = __float2bfloat16(sc);
+    kz[tid] = zb;
+    for (int t = 0; t < kKeys; ++t) {
+      const float x = __bfloat162float(K[t * kDim + tid]);
+      codes[t][tid] = static_cast<uint8_t>(fminf(fmaxf(rintf(__fdiv_rn(x - z, sc)), 0.f), levels));
+    }
+  }
+  __syncthreads();
+  {  // pack token tid's key codes: 8 (2-bit) or 2 (4-bit) codes per byte ... as words of 8 codes
+    const int per_word = bits == 2 ? 8 : 8;
+    for (int ch0 = 0; ch0 < kDim; ch0 += per_word) {
+      uint32_t w = 0;
+      for (int e = 0; e < 8; ++e) w |= static_cast<uint32_t>(codes[tid][ch0 + e]) << (e * bits);
+      if (bits == 2) *reinterpret_cast<uint16_t*>(out + tid * (kDim * 2 / 8) + ch0 / 4) = static_cast<uint16_t>(w);
+      else *reinterpret_cast<uint32_t*>(out + tid * (kDim * 4 / 8) + ch0 / 2) = w;
+    }
+  }
+  // values: token tid, groups of 32 channels
+  const bf16* vrow = V + static_cast<size_t>(tid) * kDim;
+  for (int g = 0; g < kDim / 32; ++g) {
+    float lo = INFINITY, hi = -INFINITY;
+    for (int d = 0; d < 32; ++d) {
+      const float x = __bfloat162float(vrow[g * 32 + d]);
+      lo = fminf(lo, x);
+      hi = fmaxf(hi, x);
+    }
+    const bf16 sb = __float2bfloat16((hi - lo) / levels), zb = __float2bfloat16(lo);
+    const float sc = __bfloat162float(sb) > 0.f ? __bfloat162float(sb) : 1.f, z = __bfloat162float(zb);
+    vs[tid * 4 + g] = __float2bfloat16(sc);
+    vz[tid * 4 + g] = zb;
+    for (int d0 = 0; d0 < 32; d0 += 8) {
+      uint32_t w = 0;
+      for (int e = 0; e < 8; ++e) {
+        const float x = __bfloat162float(vrow[g * 32 + d0 + e]);
+        w |= static_cast<uint32_t>(fminf(fmaxf(rintf(__fdiv_rn(x - z, sc)), 0.f), levels)) << (e * bits);
+      }
+      const int ch0 = g * 32 + d0;
+      if (bits == 2) *reinterpret_cast<uint16_t*>(vc + tid * (kDim * 2 / 8) + ch0 / 4) = static_cast<uint16_t>(w);
+      else *reinterpret_cast<uint32_t*>(vc + tid * (kDim * 4 / 8) + ch0 / 2) = w;
+    }
+  }
+}
+
+__global__ void kivi_advance_kernel(const int* __restrict__ kv_len, int* __restrict__ chunks, int B, int max_new,
+                                    int residual) {
+  pdl_trigger();
+  pdl_wait();
+  const int b = blockIdx.x * blockDim.x + threadIdx.x;
+  if (b >= B) return;
+  const int ready = max(0, (kv_len[b] - residual) / kKeys);
+  chunks[b] = max(chunks[b], min(ready, chunks[b] + max_new));
+}
+
 }  // namespace
 
 // The split over keys depends on the batch, the KV heads and the cache size only (not on the number of query
@@ -543,7 +701,8 @@ int launch_attention(const void* q, const CUtensorMap* tm_k, const CUtensorMap* 
                      const int* kv_len, const int* n_new, const int64_t* mask, int B, int T, int H, int Hkv, int D,
                      int S, float scale, int q_offset, const AttnPlan& plan, unsigned* status, cudaStream_t stream,
                      unsigned long long* trace, const float* k_scale, const float* v_scale, const uint32_t* keep,
-                     float* lse_out) {
+                     float* lse_out, const uint8_t* kivi, const int* kivi_chunks, int kivi_bits) {
+  if (kivi != nullptr && (k_scale != nullptr || (kivi_bits != 2 && kivi_bits != 4))) return -1;
   if (D != kDim || H % Hkv != 0) return -1;
   if (mask != nullptr && T > 64) return -1;
   const bool fp8 = k_scale != nullptr;
@@ -561,7 +720,7 @@ int launch_attention(const void* q, const CUtensorMap* tm_k, const CUtensorMap* 
   launch_pdl(fp8 ? attn_tc_kernel<true> : attn_tc_kernel<false>, grid, dim3(kThreads), kSmem, stream,
              static_cast<const bf16*>(q), *tm_k, *tm_v, static_cast<bf16*>(out), ws_o, ws_ml, kv_len, n_new, mask, T,
              H, Hkv, S, scale * 1.4426950408889634f, q_offset, plan.chunks_per_split, plan.m_tiles, status, trace,
-             k_scale, v_scale, keep, lse_out);
+             k_scale, v_scale, keep, lse_out, kivi, kivi_chunks, kivi_bits);
   if (plan.splits > 1) {
     dim3 mgrid(ctas, kRows / 4);
     launch_pdl(attn_merge_kernel, mgrid, dim3(128), 0, stream, static_cast<const float*>(ws_o),
@@ -585,6 +744,18 @@ int launch_attention_scores(const void* q, const CUtensorMap* tm_k, const float*
   dim3 grid(B * Hkv * m_tiles, (S + kKeys - 1) / kKeys);
   launch_pdl(attn_scores_kernel, grid, dim3(kThreads), kScoreSmem, stream, static_cast<const bf16*>(q), *tm_k, lse2,
              scores, kv_len, n_new, mask, T, H, Hkv, S, scale * 1.4426950408889634f, q_offset, m_tiles, status);
+  return 0;
+}
+
+int kivi_chunk_size(int bits) { return kivi_chunk_bytes(bits); }
+
+int launch_kivi_quantize(const void* cache, void* kivi, const int* kv_len, int* chunks, int L, int B, int Hkv, int S,
+                         int D, int bits, int residual, int max_new, cudaStream_t stream) {
+  if (D != kDim || S % kKeys != 0 || (bits != 2 && bits != 4) || max_new < 1) return -1;
+  launch_pdl(kivi_quantize_kernel, dim3(L, B * Hkv, max_new), dim3(kKeys), 0, stream,
+             static_cast<const bf16*>(cache), static_cast<uint8_t*>(kivi), kv_len, static_cast<const int*>(chunks), B,
+             Hkv, S, bits, residual);
+  launch_pdl(kivi_advance_kernel, dim3((B + 127) / 128), dim3(128), 0, stream, kv_len, chunks, B, max_new, residual);
   return 0;
 }
 

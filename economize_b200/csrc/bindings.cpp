@@ -195,7 +195,8 @@ Tensor rope_store(Tensor qkv, Tensor positions, Tensor cos, Tensor sin, int64_t 
 
 Tensor attention(Tensor q, Tensor k_cache, Tensor v_cache, Tensor kv_len, Tensor n_new, c10::optional<Tensor> mask,
                  double scale, int64_t q_offset, c10::optional<Tensor> trace, c10::optional<Tensor> k_scale,
-                 c10::optional<Tensor> v_scale, c10::optional<Tensor> keep, c10::optional<Tensor> lse_out) {
+                 c10::optional<Tensor> v_scale, c10::optional<Tensor> keep, c10::optional<Tensor> lse_out,
+                 c10::optional<Tensor> kivi, c10::optional<Tensor> kivi_chunks, int64_t kivi_bits) {
   CHECK_CUDA(q);
   CHECK_BF16(q);
   TORCH_CHECK(q.dim() == 4 && q.size(3) == 128 && k_cache.dim() == 4, "attention: head_dim must be 128");
@@ -223,6 +224,13 @@ Tensor attention(Tensor q, Tensor k_cache, Tensor v_cache, Tensor kv_len, Tensor
     TORCH_CHECK(keep->is_contiguous() && keep->numel() == static_cast<int64_t>(B) * Hkv * (S / 32),
                 "keep must be int32 [B, Hkv, S / 32] bit words");
   }
+  if (kivi.has_value()) {
+    TORCH_CHECK(kivi->scalar_type() == at::kByte && kivi->is_contiguous() && kivi_chunks.has_value(),
+                "kivi storage must be contiguous uint8 with chunk counts");
+    TORCH_CHECK(kivi->numel() == static_cast<int64_t>(B) * Hkv * (S / 128) * ecz::kivi_chunk_size(kivi_bits),
+                "kivi storage must be [B, Hkv, S / 128, chunk bytes]");
+    CHECK_I32(*kivi_chunks);
+  }
   if (lse_out.has_value()) {
     TORCH_CHECK(lse_out->scalar_type() == at::kFloat && lse_out->is_contiguous() &&
                     lse_out->numel() == static_cast<int64_t>(B) * T * H,
@@ -249,7 +257,10 @@ Tensor attention(Tensor q, Tensor k_cache, Tensor v_cache, Tensor kv_len, Tensor
                                        fp8 ? v_scale->data_ptr<float>() : nullptr,
                                        keep.has_value() ? reinterpret_cast<const uint32_t*>(keep->data_ptr<int>())
                                                         : nullptr,
-                                       lse_out.has_value() ? lse_out->data_ptr<float>() : nullptr);
+                                       lse_out.has_value() ? lse_out->data_ptr<float>() : nullptr,
+                                       kivi.has_value() ? kivi->data_ptr<uint8_t>() : nullptr,
+                                       kivi.has_value() ? kivi_chunks->data_ptr<int>() : nullptr,
+                                       static_cast<int>(kivi_bits));
   TORCH_CHECK(rc == 0, "attention: unsupported shape (head_dim must be 128, H divisible by H_kv)");
   return out;
 }
@@ -555,6 +566,26 @@ void attention_scores(Tensor q, Tensor k_cache, Tensor kv_len, Tensor n_new, c10
   TORCH_CHECK(rc == 0, "attention_scores: unsupported shape");
 }
 
+void kivi_quantize(Tensor cache, Tensor kivi, Tensor kv_len, Tensor chunks, int64_t bits, int64_t residual,
+                   int64_t max_new) {
+  CHECK_CUDA(cache);
+  CHECK_BF16(cache);
+  CHECK_I32(kv_len);
+  CHECK_I32(chunks);
+  TORCH_CHECK(cache.dim() == 6 && cache.is_contiguous(), "cache must be a contiguous [L, 2, B, Hkv, S, D] tensor");
+  c10::cuda::CUDAGuard guard(cache.device());
+  const int L = static_cast<int>(cache.size(0)), B = static_cast<int>(cache.size(2)), Hkv = static_cast<int>(cache.size(3));
+  const int S = static_cast<int>(cache.size(4)), D = static_cast<int>(cache.size(5));
+  TORCH_CHECK(kivi.scalar_type() == at::kByte && kivi.is_contiguous() &&
+                  kivi.numel() == static_cast<int64_t>(L) * B * Hkv * (S / 128) * ecz::kivi_chunk_size(bits),
+              "kivi storage must be [L, B, Hkv, S / 128, chunk bytes]");
+  const int rc = ecz::launch_kivi_quantize(cache.data_ptr(), kivi.data_ptr(), kv_len.data_ptr<int>(),
+                                           chunks.data_ptr<int>(), L, B, Hkv, S, D, static_cast<int>(bits),
+                                           static_cast<int>(residual), static_cast<int>(max_new),
+                                           at::cuda::getCurrentCUDAStream());
+  TORCH_CHECK(rc == 0, "kivi_quantize: head_dim 128, 2 or 4 bits");
+}
+
 // Explicit GEMM variant (tuning and benchmarks): mode 1 cluster split-K (DSMEM reduction), 2 split-K through a
 // global fp32 workspace reduced by the tile's last CTA, 3 persistent stream-K; splits <= 0 picks the default.
 Tensor linear_variant(Tensor x, Tensor w, int64_t mode, int64_t splits) {
@@ -842,7 +873,10 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("attention", &attention, "tree-masked / causal attention over the slot cache (tcgen05; bf16 or fp8 KV)",
         py::arg("q"), py::arg("k_cache"), py::arg("v_cache"), py::arg("kv_len"), py::arg("n_new"), py::arg("mask"),
         py::arg("scale"), py::arg("q_offset"), py::arg("trace") = py::none(), py::arg("k_scale") = py::none(),
-        py::arg("v_scale") = py::none(), py::arg("keep") = py::none(), py::arg("lse_out") = py::none());
+        py::arg("v_scale") = py::none(), py::arg("keep") = py::none(), py::arg("lse_out") = py::none(),
+        py::arg("kivi") = py::none(), py::arg("kivi_chunks") = py::none(), py::arg("kivi_bits") = 0);
+  m.def("kivi_chunk_size", &ecz::kivi_chunk_size, "bytes of one KIVI-coded 128-key chunk");
+  m.def("kivi_quantize", &kivi_quantize, "quantise committed cache chunks to KIVI codes and advance the counts");
   m.def("attention_scores", &attention_scores, "accumulate KV-eviction attention scores (tcgen05)");
   m.def("silu_mul", &silu_mul, "SwiGLU activation of [gate; up]");
   m.def("linear_parts", &linear_parts, "x @ w.T as bf16 or fp32 split-K partials for a fusing consumer");

@@ -78,7 +78,13 @@ int launch_attention(const void* q, const CUtensorMap* tm_k, const CUtensorMap* 
                      const int* kv_len, const int* n_new, const int64_t* mask, int B, int T, int H, int Hkv, int D,
                      int S, float scale, int q_offset, const AttnPlan& plan, unsigned* status, cudaStream_t stream,
                      unsigned long long* trace = nullptr, const float* k_scale = nullptr,
-                     const float* v_scale = nullptr, const uint32_t* keep = nullptr, float* lse_out = nullptr);
+                     const float* v_scale = nullptr, const uint32_t* keep = nullptr, float* lse_out = nullptr,
+                     const uint8_t* kivi = nullptr, const int* kivi_chunks = nullptr, int kivi_bits = 0);
+// KIVI: bytes of one quantized 128-key chunk; quantise committed chunks of a bf16 cache [L, 2, B, Hkv, S, D] into
+// kivi [L, B, Hkv, S / 128, chunk bytes] and advance chunks [B] (at most max_new chunks per row and call)
+int kivi_chunk_size(int bits);
+int launch_kivi_quantize(const void* cache, void* kivi, const int* kv_len, int* chunks, int L, int B, int Hkv, int S,
+                         int D, int bits, int residual, int max_new, cudaStream_t stream);
 // KV-eviction scores: scores[b, kvh, s] += attention probability mass of slot s (see attention.cu)
 int launch_attention_scores(const void* q, const CUtensorMap* tm_k, const float* lse2, float* scores,
                             const int* kv_len, const int* n_new, const int64_t* mask, int B, int T, int H, int Hkv,

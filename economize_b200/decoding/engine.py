@@ -220,6 +220,7 @@ class SpecEngine:
         batch, width = prompts.shape
         capture = drafter.capture_layers if drafter is not None else ()
         chunk = self.config.prefill_chunk
+        model.begin_sequence(st.cache)
         if chunk is not None and width > chunk:
             hidden, aux = self._chunked_prefill(st, prompts, lengths, chunk, capture)
         else:
@@ -228,6 +229,7 @@ class SpecEngine:
         rows = torch.arange(batch, device=prompts.device)
         bonus = self._pred(hidden[rows, last_idx])
         st.kv_len.copy_(lengths)
+        model.after_commit(st.cache, st.kv_len, prefill=True)
         st.last.copy_(bonus)
         st.history.zero_()
         st.history[:, :width] = prompts
@@ -311,6 +313,7 @@ class SpecEngine:
             self._plain_cycle(st)
         else:
             self._spec_cycle(st)
+        self.model.after_commit(st.cache, st.kv_len)  # KV coders compress what became old (inside the graph)
 
     def _plain_cycle(self, st: _State) -> None:
         model = self.model

@@ -81,6 +81,8 @@ class CausalLM(nn.Module):
         self.kv_dtype: torch.dtype | None = None
         #: KV eviction policy (a kv_evict technique): scores the prompt at prefill, hides evicted slots afterwards
         self.kv_evictor = None
+        #: KV coder (kivi): codes committed chunks after every commit; attention reads the codes
+        self.kv_quantizer = None
         self.kv_scales: tuple[torch.Tensor, torch.Tensor] | None = None
         #: tensor-parallel group (set by economize_b200.parallel.tp.shard_model) and this rank's shard sizes
         self.tp = None
@@ -189,8 +191,9 @@ class CausalLM(nn.Module):
                            v_cache, batch.kv_len, batch.n_new, layer.q_norm, layer.k_norm, c.rms_norm_eps,
                            q_offset=batch.q_offset, k_scale=k_scale, v_scale=v_scale)
         keep = self.kv_evictor.keep_for(index, k_cache, q, batch) if self.kv_evictor is not None else None
+        kivi = self.kv_quantizer.layer_args(index, cache) if self.kv_quantizer is not None else {}
         o = ops.attention(q, k_cache, v_cache, batch.kv_len, batch.n_new, batch.mask, q_offset=batch.q_offset,
-                          k_scale=k_scale, v_scale=v_scale, keep=keep)
+                          k_scale=k_scale, v_scale=v_scale, keep=keep, **kivi)
         if self.kv_evictor is not None and batch.is_prefill:
             self.kv_evictor.observe_prefill(index, q, k_cache, v_cache, batch)
         o = o.reshape(*o.shape[:2], -1)
@@ -227,6 +230,16 @@ class CausalLM(nn.Module):
         if self.observer is not None:
             self.observer(index, "w_down", a)
         return self._row_linear(a, layer.w_down)
+
+    def begin_sequence(self, cache: KVCache) -> None:
+        """A new generation starts in ``cache`` (slot 0 on)."""
+        if self.kv_quantizer is not None:
+            self.kv_quantizer.reset(cache)
+
+    def after_commit(self, cache: KVCache, kv_len: torch.Tensor, prefill: bool = False) -> None:
+        """Tokens up to ``kv_len`` are committed (KV coders compress what became old)."""
+        if self.kv_quantizer is not None:
+            self.kv_quantizer.after_commit(cache, kv_len, max(1, cache.capacity // 128) if prefill else 1)
 
     def logits(self, hidden: torch.Tensor) -> torch.Tensor:
         """Logits over the full vocabulary (gathered from the vocabulary shards under tensor parallelism)."""

@@ -21,6 +21,7 @@ __all__ = [
     "attention_scores",
     "available",
     "greedy_accept",
+    "kivi_quantize",
     "kv_compact",
     "linear",
     "linear_parts",
@@ -121,16 +122,27 @@ def attention(q: torch.Tensor, k_cache: torch.Tensor, v_cache: torch.Tensor, kv_
               n_new: torch.Tensor, mask: torch.Tensor | None = None, scale: float | None = None,
               q_offset: int = 0, k_scale: torch.Tensor | None = None,
               v_scale: torch.Tensor | None = None, keep: torch.Tensor | None = None,
-              lse_out: torch.Tensor | None = None) -> torch.Tensor:
+              lse_out: torch.Tensor | None = None, kivi: torch.Tensor | None = None,
+              kivi_chunks: torch.Tensor | None = None, kivi_bits: int = 0) -> torch.Tensor:
     """Causal / tree-masked attention over the slot cache (see :func:`.reference.attention`); fp8 caches take
     per-KV-head scales, ``keep`` (int32 bit words ``[B, H_kv, S / 32]``) hides evicted committed slots and
     ``lse_out [B, T, H]`` receives every row's log2-domain log-sum-exp."""
     scale = float(scale if scale is not None else q.shape[-1] ** -0.5)
     if q.is_cuda:
         return require().attention(q, k_cache, v_cache, kv_len, n_new, mask, scale, int(q_offset), None, k_scale,
-                                   v_scale, keep, lse_out)
+                                   v_scale, keep, lse_out, kivi, kivi_chunks, int(kivi_bits))
     return reference.attention(q, k_cache, v_cache, kv_len, n_new, mask, scale, q_offset=q_offset, k_scale=k_scale,
-                               v_scale=v_scale, keep=keep, lse_out=lse_out)
+                               v_scale=v_scale, keep=keep, lse_out=lse_out, kivi=kivi, kivi_chunks=kivi_chunks,
+                               kivi_bits=kivi_bits)
+
+
+def kivi_quantize(cache: torch.Tensor, kivi: torch.Tensor, kv_len: torch.Tensor, chunks: torch.Tensor, bits: int,
+                  residual: int, max_new: int) -> None:
+    """Code newly committed 128-key chunks of every layer into KIVI storage and advance ``chunks`` (in place)."""
+    if cache.is_cuda:
+        require().kivi_quantize(cache, kivi, kv_len, chunks, int(bits), int(residual), int(max_new))
+        return
+    reference.kivi_quantize(cache, kivi, kv_len, chunks, bits, residual, max_new)
 
 
 def attention_scores(q: torch.Tensor, k_cache: torch.Tensor, kv_len: torch.Tensor, n_new: torch.Tensor,

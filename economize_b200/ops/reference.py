@@ -98,7 +98,8 @@ def attention(q: torch.Tensor, k_cache: torch.Tensor, v_cache: torch.Tensor, kv_
               n_new: torch.Tensor, mask: torch.Tensor | None = None, scale: float | None = None,
               softcap: float | None = None, q_offset: int = 0, k_scale: torch.Tensor | None = None,
               v_scale: torch.Tensor | None = None, keep: torch.Tensor | None = None,
-              lse_out: torch.Tensor | None = None) -> torch.Tensor:
+              lse_out: torch.Tensor | None = None, kivi: torch.Tensor | None = None,
+              kivi_chunks: torch.Tensor | None = None, kivi_bits: int = 0) -> torch.Tensor:
     """Attention of queries ``[B, T, H, D]`` over the slot cache ``[B, H_kv, S, D]`` (bf16, fp32, or e4m3 codes with
     per-KV-head scales ``k_scale``/``v_scale``).
 
@@ -115,6 +116,15 @@ def attention(q: torch.Tensor, k_cache: torch.Tensor, v_cache: torch.Tensor, kv_
     if k_scale is not None:
         keys = keys * k_scale.float()[None, :, None, None]
         values = values * v_scale.float()[None, :, None, None]
+    if kivi is not None:  # KIVI-coded chunks replace the bf16 entries of their slots
+        from .kivi import dequant_chunks
+
+        dk, dv = dequant_chunks(kivi, kivi_bits, dim)  # [B, H_kv, C, 128, D]
+        for b in range(batch):
+            n = int(kivi_chunks[b]) * 128
+            if n:
+                keys[b, :, :n] = dk[b, :, : n // 128].reshape(kv_heads, n, dim)
+                values[b, :, :n] = dv[b, :, : n // 128].reshape(kv_heads, n, dim)
     group = heads // kv_heads
     keys = keys.repeat_interleave(group, 1)
     values = values.repeat_interleave(group, 1)
@@ -291,3 +301,20 @@ def attention_scores(q: torch.Tensor, k_cache: torch.Tensor, kv_len: torch.Tenso
     s = torch.matmul(q.float().transpose(1, 2), keys.transpose(-1, -2)) * scale * 1.4426950408889634
     p = torch.exp2(s - lse2.float().transpose(1, 2)[..., None]).masked_fill(~vis[:, None], 0.0)
     scores += p.sum(2).reshape(batch, kv_heads, group, width).sum(2)
+
+
+def kivi_quantize(cache: torch.Tensor, kivi: torch.Tensor, kv_len: torch.Tensor, chunks: torch.Tensor, bits: int,
+                  residual: int, max_new: int) -> None:
+    """Code the committed chunks ``chunks[b] .. `` of ``cache [L, 2, B, H_kv, S, D]`` that lie at least
+    ``residual`` slots behind ``kv_len[b]`` (at most ``max_new`` per row) into ``kivi [L, B, H_kv, S/128, bytes]``."""
+    from .kivi import pack_chunks
+
+    for b in range(cache.shape[2]):
+        ready = max(0, (int(kv_len[b]) - residual) // 128)
+        start = int(chunks[b])
+        stop = min(ready, start + max_new)
+        for c in range(start, stop):
+            k = cache[:, 0, b, :, c * 128:(c + 1) * 128]
+            v = cache[:, 1, b, :, c * 128:(c + 1) * 128]
+            kivi[:, b, :, c] = pack_chunks(k, v, bits)
+        chunks[b] = max(start, stop)

@@ -1,4 +1,5 @@
-"""KV-cache quantization: ``kv_fp8`` / ``kv_fp8_fused`` (e4m3 codes with static per-head, per-layer or unit scales,
+"""KV-cache quantization: ``kivi`` / ``kivi_fused`` (2- or 4-bit KIVI chunks dequantised inside the attention
+kernel) and ``kv_fp8`` / ``kv_fp8_fused`` (e4m3 codes with static per-head, per-layer or unit scales,
 read directly by the tcgen05 attention kernel) (economize ``techniques/kv_quant/fp8.py:55-270`` and
 ``techniques/kv_fp8_fused``).
 
@@ -19,7 +20,8 @@ from ...core.technique import Capability, Family, Technique, TechniqueConfig, re
 from ...errors import ConfigError
 from ...validation import check_choice
 
-__all__ = ["KVFp8Config", "KVFp8FusedConfig", "KVFp8Technique", "calibrate_kv_scales"]
+__all__ = ["KIVIConfig", "KIVIFusedConfig", "KIVITechnique", "KVFp8Config", "KVFp8FusedConfig", "KVFp8Technique",
+           "calibrate_kv_scales"]
 
 E4M3_MAX = 448.0
 
@@ -125,3 +127,85 @@ class KVFp8Technique(Technique):
 @register_technique
 class KVFp8FusedTechnique(KVFp8Technique):
     config_class = KVFp8FusedConfig
+
+
+# ---- KIVI ------------------------------------------------------------------------------------------------------
+@dataclass(frozen=True)
+class KIVIConfig(TechniqueConfig):
+    """KIVI-coded KV cache (Liu et al., 2024; economize ``kivi``/``kivi_fused``, ``kv_quant/packed.py``).
+
+    Args:
+        bits: 2 or 4.
+        residual: Most recent committed tokens kept in bf16 (at least this many; coding happens in 128-key chunks).
+    """
+
+    technique: ClassVar[str] = "kivi"
+    bits: int = 2
+    residual: int = 128
+
+    def __post_init__(self) -> None:
+        check_choice("bits", self.bits, (2, 4))
+        if self.residual < 0:
+            raise ConfigError("residual must be >= 0")
+
+
+@dataclass(frozen=True)
+class KIVIFusedConfig(KIVIConfig):
+    technique: ClassVar[str] = "kivi_fused"
+
+
+@register_technique
+class KIVITechnique(Technique):
+    """Codes committed chunks after every commit (one kernel per cycle, inside the captured graph) and hands the
+    attention kernel the coded chunks, which it dequantises in shared memory. The bf16 cache keeps every slot (the
+    drafters and KV compaction address it by slot), so the saving is in the bytes attention reads."""
+
+    config_class = KIVIConfig
+    capabilities = Capability.KV_CACHE
+    family = Family.KV_COMPRESSION
+    lossless = False
+
+    def __init__(self, config: KIVIConfig, model) -> None:
+        super().__init__(config, model)
+        self._store: dict[int, tuple[torch.Tensor, torch.Tensor]] = {}
+
+    def attach(self) -> None:
+        if self.model.kv_dtype is not None:
+            raise ConfigError("kivi codes a bf16 cache; it cannot be combined with kv_fp8")
+        self.model.kv_quantizer = self
+
+    def detach(self) -> None:
+        self.model.kv_quantizer = None
+
+    def storage(self, cache) -> tuple[torch.Tensor, torch.Tensor]:
+        from ...ops.kivi import chunk_bytes
+
+        key = id(cache.data)
+        st = self._store.get(key)
+        L, _, B, hkv, S, _ = cache.data.shape
+        if st is None or st[0].shape[:4] != (L, B, hkv, S // 128):
+            dim = cache.data.shape[-1]
+            st = (torch.zeros(L, B, hkv, S // 128, chunk_bytes(self.config.bits, dim), dtype=torch.uint8,
+                              device=cache.data.device),
+                  torch.zeros(B, dtype=torch.int32, device=cache.data.device))
+            self._store = {key: st}  # one live cache at a time
+        return st
+
+    def layer_args(self, layer: int, cache) -> dict:
+        data, chunks = self.storage(cache)
+        return {"kivi": data[layer], "kivi_chunks": chunks, "kivi_bits": self.config.bits}
+
+    def reset(self, cache) -> None:
+        self.storage(cache)[1].zero_()
+
+    def after_commit(self, cache, kv_len: torch.Tensor, max_new: int = 1) -> None:
+        from ... import ops
+
+        data, chunks = self.storage(cache)
+        ops.kivi_quantize(cache.data, data, kv_len.to(torch.int32), chunks, self.config.bits, self.config.residual,
+                          max_new)
+
+
+@register_technique
+class KIVIFusedTechnique(KIVITechnique):
+    config_class = KIVIFusedConfig

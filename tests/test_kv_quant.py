@@ -121,3 +121,57 @@ def test_fp8_engine_decodes_on_gpu(cuda):
     plain = eff.decode(p, 16, decoding=eco.DecodeConfig(cycle_length=1)).tokens
     spec = eff.decode(p, 16).tokens
     assert torch.equal(spec.cpu(), plain.cpu())
+
+
+# ---- KIVI -----------------------------------------------------------------------------------------------------
+def test_kivi_pack_roundtrip_error():
+    from economize_b200.ops.kivi import dequant_chunks, pack_chunks
+
+    g = torch.Generator().manual_seed(0)
+    k = torch.randn(1, 2, 128, 128, generator=g).bfloat16()
+    v = torch.randn(1, 2, 128, 128, generator=g).bfloat16()
+    kk, vv = dequant_chunks(pack_chunks(k, v, 4), 4)
+    assert (kk - k.float()).norm() / k.float().norm() < 0.12
+    assert (vv - v.float()).norm() / v.float().norm() < 0.1
+
+
+def test_kivi_model_decodes_losslessly():
+    from economize_b200.techniques.kv_quant import KIVIConfig
+
+    model = tiny_model()
+    eff = eco.apply(model, KIVIConfig(bits=4, residual=16), Eagle3Config(), decoding=eco.DecodeConfig(cycle_length=4))
+    p = prompts((300,))[0]
+    spec = eff.decode(p, 8).tokens
+    plain = eff.decode(p, 8, decoding=eco.DecodeConfig(cycle_length=1)).tokens
+    assert torch.equal(spec, plain)
+    tech = eff.techniques["kivi"]
+    data, chunks = next(iter(tech._store.values()))
+    assert int(chunks[0]) == (300 + 8 - 16) // 128  # the prompt's old chunks (and any that aged since) are coded
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("bits", [2, 4])
+def test_kivi_kernels_match_reference(cuda, bits):
+    from economize_b200.ops.kivi import chunk_bytes
+
+    g = torch.Generator(device=cuda).manual_seed(0)
+    L, B, Hkv, S, D, H, T = 2, 2, 2, 512, 128, 8, 7
+    cache = torch.randn(L, 2, B, Hkv, S, D, device=cuda, generator=g).bfloat16()
+    kv_len = torch.tensor([400, 300], dtype=torch.int32, device=cuda)
+    outs = {}
+    for name, fn in (("kernel", ops.kivi_quantize), ("ref", ref.kivi_quantize)):
+        kivi = torch.zeros(L, B, Hkv, S // 128, chunk_bytes(bits), dtype=torch.uint8, device=cuda)
+        chunks = torch.zeros(B, dtype=torch.int32, device=cuda)
+        fn(cache, kivi, kv_len, chunks, bits, 64, 8)
+        outs[name] = (kivi, chunks)
+    assert outs["kernel"][1].tolist() == [2, 1] == outs["ref"][1].tolist()
+    assert torch.equal(outs["kernel"][0], outs["ref"][0])
+    kivi, chunks = outs["kernel"]
+    q = torch.randn(B, T, H, D, device=cuda, generator=g).bfloat16()
+    n_new = torch.full((B,), T, dtype=torch.int32, device=cuda)
+    for layer in range(L):
+        k, v = cache[layer, 0], cache[layer, 1]
+        got = ops.attention(q, k, v, kv_len, n_new, None, kivi=kivi[layer], kivi_chunks=chunks, kivi_bits=bits)
+        exp = ref.attention(q.float(), k, v, kv_len, n_new, None, kivi=kivi[layer], kivi_chunks=chunks,
+                            kivi_bits=bits)
+        torch.testing.assert_close(got.float(), exp.float(), atol=2e-2, rtol=2e-2)
