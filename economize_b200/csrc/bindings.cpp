@@ -779,6 +779,69 @@ ecz::PeerPtrs peer_ptrs(const std::vector<int64_t>& ptrs) {
   return p;
 }
 
+// ---- expert parallelism over NVLink peer memory (ep.cu) ---------------------------------------------------------
+int64_t ep_buffer_bytes(int64_t world, int64_t experts_local, int64_t cap, int64_t hidden, int64_t ret_rows) {
+  return ecz::ep_layout(static_cast<int>(world), static_cast<int>(experts_local), static_cast<int>(cap),
+                        static_cast<int>(hidden), static_cast<int>(ret_rows)).bytes;
+}
+
+// One expert-parallel MoE MLP: xs [T k, H] are this rank's routed rows in global expert order (moe_gather), offsets
+// [E + 1] the global expert offsets, pos / w [T, k] each pair's row and weight; w_gate_up [E_l, 2F, H] and w_down
+// [E_l, H, F] this rank's experts. Dispatch, the two grouped GEMMs, combine and the weighted sum run on the device.
+Tensor ep_moe(Tensor xs, Tensor offsets, Tensor pos, Tensor w, Tensor w_gate_up, Tensor w_down,
+              std::vector<int64_t> ptrs, int64_t rank, int64_t cap, int64_t ret_rows) {
+  CHECK_CUDA(xs);
+  CHECK_BF16(xs);
+  CHECK_BF16(w_gate_up);
+  CHECK_BF16(w_down);
+  CHECK_I32(offsets);
+  CHECK_I32(pos);
+  TORCH_CHECK(w.scalar_type() == at::kFloat, "ep_moe: fp32 routing weights");
+  c10::cuda::CUDAGuard guard(xs.device());
+  xs = xs.contiguous();
+  const int world = static_cast<int>(ptrs.size());
+  const int El = static_cast<int>(w_gate_up.size(0)), F2 = static_cast<int>(w_gate_up.size(1));
+  const int H = static_cast<int>(xs.size(1)), T = static_cast<int>(pos.size(0)), k = static_cast<int>(pos.size(1));
+  TORCH_CHECK(offsets.numel() == static_cast<int64_t>(world) * El + 1, "ep_moe: offsets must cover world x E_l");
+  TORCH_CHECK(w_gate_up.size(2) == H && w_down.size(0) == El && w_down.size(1) == H && w_down.size(2) * 2 == F2,
+              "ep_moe: expert weight shapes");
+  TORCH_CHECK(xs.size(0) == static_cast<int64_t>(T) * k && T * k <= cap && T * k <= ret_rows,
+              "ep_moe: more routed rows than the buffers hold");
+  const ecz::EpLayout L = ecz::ep_layout(world, El, static_cast<int>(cap), H, static_cast<int>(ret_rows));
+  const ecz::PeerPtrs peers = peer_ptrs(ptrs);
+  cudaStream_t stream = at::cuda::getCurrentCUDAStream();
+  unsigned* status = status_word(xs.device());
+  auto out = at::empty({T, H}, xs.options());
+  const int G = world * El, R = world * static_cast<int>(cap), F = F2 / 2;
+  auto seg = at::empty({3, G}, offsets.options());
+  int* s0 = seg.data_ptr<int>();
+  TORCH_CHECK(ecz::launch_ep_dispatch(xs.data_ptr(), offsets.data_ptr<int>(), peers, L, static_cast<int>(rank),
+                                      T * k, stream) == 0, "ep_moe: dispatch launch failed");
+  TORCH_CHECK(ecz::launch_ep_segments(peers, L, static_cast<int>(rank), s0, s0 + G, s0 + 2 * G, status, stream) == 0,
+              "ep_moe: at most 128 (rank, expert) segments");
+  void* recv = static_cast<uint8_t*>(reinterpret_cast<void*>(ptrs[rank])) + L.recv_off;
+  const int bn = ecz::grouped_block_n(static_cast<int>(cap), G);
+  auto gu = at::empty({R, F2}, xs.options());
+  w_gate_up = w_gate_up.contiguous();
+  w_down = w_down.contiguous();
+  const CUtensorMap* tw1 = tensor_map(w_gate_up.data_ptr(), static_cast<uint64_t>(El) * F2, H, H, 128);
+  const CUtensorMap* tx1 = tensor_map(recv, R, H, H, bn);
+  TORCH_CHECK(ecz::launch_gemm_segments(tw1, tx1, gu.data_ptr(), s0, s0 + G, s0 + 2 * G, G, static_cast<int>(cap), F2,
+                                        H, status, stream) == 0, "ep_moe: H must be a multiple of 64");
+  auto a = at::empty({R, F}, xs.options());
+  TORCH_CHECK(ecz::launch_silu_mul(gu.data_ptr(), a.data_ptr(), R, F, stream) == 0, "ep_moe: silu_mul failed");
+  auto y = at::empty({R, H}, xs.options());
+  const CUtensorMap* tw2 = tensor_map(w_down.data_ptr(), static_cast<uint64_t>(El) * H, F, F, 128);
+  const CUtensorMap* tx2 = tensor_map(a.data_ptr(), R, F, F, bn);
+  TORCH_CHECK(ecz::launch_gemm_segments(tw2, tx2, y.data_ptr(), s0, s0 + G, s0 + 2 * G, G, static_cast<int>(cap), H,
+                                        F, status, stream) == 0, "ep_moe: F must be a multiple of 64");
+  TORCH_CHECK(ecz::launch_ep_combine(y.data_ptr(), s0, s0 + G, peers, L, static_cast<int>(rank), stream) == 0,
+              "ep_moe: combine launch failed");
+  TORCH_CHECK(ecz::launch_ep_finish(peers, L, static_cast<int>(rank), pos.data_ptr<int>(), w.data_ptr<float>(),
+                                    out.data_ptr(), T, k, status, stream) == 0, "ep_moe: finish launch failed");
+  return out;
+}
+
 // Row-parallel GEMM whose output tiles go straight into every peer's slot (tensor-parallel push mode).
 void linear_push(Tensor x, Tensor w, std::vector<int64_t> ptrs, int64_t rank, int64_t parity, int64_t slot_elems) {
   CHECK_CUDA(x);
@@ -903,6 +966,8 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("sample", &sample, "inverse-CDF draw of one token per probability row");
   m.def("rejection", &rejection, "lossless speculative sampling of a draft chain (accept/reject + resample)");
   m.def("ngram", &ngram, "prompt-lookup draft proposals from the token history");
+  m.def("ep_buffer_bytes", &ep_buffer_bytes, "bytes of one rank's expert-parallel symmetric buffer");
+  m.def("ep_moe", &ep_moe, "expert-parallel MoE MLP with NVLink peer-store dispatch and combine");
   m.def("symm_alloc", &symm_alloc, "cudaMalloc an IPC-exportable buffer: (pointer, handle)");
   m.def("symm_open", &symm_open, "map a peer's buffer from its IPC handle");
   m.def("symm_close", &symm_close, "unmap a peer's buffer");

@@ -139,6 +139,25 @@ int launch_act_quant_fp8(const void* x, void* q, float* sx, int M, int K, int sx
 int launch_gemm_fp8(const CUtensorMap* tm_w, const CUtensorMap* tm_x, const CUtensorMap* tm_sx, const float* sw,
                     void* y, float* ws, int M, int N, int K, int splits, unsigned* status, cudaStream_t stream);
 
+int launch_gemm_segments(const CUtensorMap* tm_w, const CUtensorMap* tm_x, void* y, const int* seg_start,
+                         const int* seg_end, const int* seg_expert, int G, int max_rows, int N, int K,
+                         unsigned* status, cudaStream_t stream);
+
+// ep.cu: expert-parallel dispatch / combine over IPC-mapped symmetric buffers (layout below, per rank).
+struct EpLayout {
+  int world = 1, experts_local = 1, cap = 1, hidden = 8, ret_rows = 1;
+  long counts_off = 0, meta_off = 0, recv_off = 0, ret_off = 0, bytes = 0;
+};
+EpLayout ep_layout(int world, int experts_local, int cap, int hidden, int ret_rows);
+int launch_ep_dispatch(const void* xs, const int* offsets, const PeerPtrs& peers, const EpLayout& L, int rank,
+                       int rows, cudaStream_t stream);
+int launch_ep_segments(const PeerPtrs& peers, const EpLayout& L, int rank, int* seg_start, int* seg_end,
+                       int* seg_expert, unsigned* status, cudaStream_t stream);
+int launch_ep_combine(const void* y, const int* seg_start, const int* seg_end, const PeerPtrs& peers,
+                      const EpLayout& L, int rank, cudaStream_t stream);
+int launch_ep_finish(const PeerPtrs& peers, const EpLayout& L, int rank, const int* pos, const float* w, void* out,
+                     int tokens, int k, unsigned* status, cudaStream_t stream);
+
 // tmap.cpp: a 2-D tensor map over a row-major [rows, cols] matrix of 1- or 2-byte elements (elem_bytes), with a
 // {box_cols, box_rows} box and the given swizzle (0, 32, 64 or 128 bytes). Returns 0 on success.
 int make_tmap_2d(CUtensorMap* map, int elem_bytes, const void* base, uint64_t rows, uint64_t cols,

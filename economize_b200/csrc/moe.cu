@@ -131,7 +131,8 @@ struct GroupedCfg {
 template <int BN>
 __global__ void __launch_bounds__(128, 2)
     gemm_grouped_kernel(const __grid_constant__ CUtensorMap tm_w, const __grid_constant__ CUtensorMap tm_x,
-                        bf16* __restrict__ y, const int* __restrict__ offsets, int N, int K, unsigned* status) {
+                        bf16* __restrict__ y, const int* __restrict__ seg_start, const int* __restrict__ seg_end,
+                        const int* __restrict__ seg_expert, int N, int K, unsigned* status) {
   using Cfg = GroupedCfg<BN>;
   constexpr int S = Cfg::kStages;
   extern __shared__ uint8_t smem_raw[];
@@ -145,10 +146,11 @@ __global__ void __launch_bounds__(128, 2)
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
   pdl_trigger();
-  pdl_wait();  // the offsets come from the routing kernel
-  const int e = blockIdx.z;
-  const int row_end = offsets[e + 1];
-  const int m0 = offsets[e] + blockIdx.y * BN;
+  pdl_wait();  // the segments come from the routing (or expert-parallel dispatch) kernel
+  const int g = blockIdx.z;  // segment: rows [seg_start[g], seg_end[g]) use expert seg_expert[g] (default g)
+  const int e = seg_expert != nullptr ? seg_expert[g] : g;
+  const int row_end = seg_end[g];
+  const int m0 = seg_start[g] + blockIdx.y * BN;
   if (m0 >= row_end) return;  // uniform: the whole CTA leaves before any shared state exists
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int n_local = blockIdx.x * kBM;
@@ -225,17 +227,17 @@ __global__ void __launch_bounds__(128, 2)
 }
 
 template <int BN>
-int run_grouped(const CUtensorMap& tm_w, const CUtensorMap& tm_x, void* y, const int* offsets, int E, int max_rows,
-                int N, int K, unsigned* status, cudaStream_t stream) {
+int run_grouped(const CUtensorMap& tm_w, const CUtensorMap& tm_x, void* y, const int* seg_start, const int* seg_end,
+                const int* seg_expert, int G, int max_rows, int N, int K, unsigned* status, cudaStream_t stream) {
   using Cfg = GroupedCfg<BN>;
   static bool configured = false;
   if (!configured) {
     cudaFuncSetAttribute(gemm_grouped_kernel<BN>, cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg::kSmem);
     configured = true;
   }
-  dim3 grid((N + kBM - 1) / kBM, (max_rows + BN - 1) / BN, E);
+  dim3 grid((N + kBM - 1) / kBM, (max_rows + BN - 1) / BN, G);
   launch_pdl(gemm_grouped_kernel<BN>, grid, dim3(128), Cfg::kSmem, stream, tm_w, tm_x, static_cast<bf16*>(y),
-             offsets, N, K, status);
+             seg_start, seg_end, seg_expert, N, K, status);
   return 0;
 }
 
@@ -275,9 +277,23 @@ int launch_gemm_grouped(const CUtensorMap* tm_w, const CUtensorMap* tm_x, void* 
                         int rows, int N, int K, unsigned* status, cudaStream_t stream) {
   if (K % kBK != 0 || N % 8 != 0 || rows < 1) return -1;
   switch (grouped_block_n(rows, E)) {
-    case 32: return run_grouped<32>(*tm_w, *tm_x, y, offsets, E, rows, N, K, status, stream);
-    case 64: return run_grouped<64>(*tm_w, *tm_x, y, offsets, E, rows, N, K, status, stream);
-    default: return run_grouped<128>(*tm_w, *tm_x, y, offsets, E, rows, N, K, status, stream);
+    case 32: return run_grouped<32>(*tm_w, *tm_x, y, offsets, offsets + 1, nullptr, E, rows, N, K, status, stream);
+    case 64: return run_grouped<64>(*tm_w, *tm_x, y, offsets, offsets + 1, nullptr, E, rows, N, K, status, stream);
+    default: return run_grouped<128>(*tm_w, *tm_x, y, offsets, offsets + 1, nullptr, E, rows, N, K, status, stream);
+  }
+}
+
+// Segments (start, end, expert) instead of expert offsets: rows of one segment use one expert's weights; at most
+// `max_rows` rows per segment.
+int launch_gemm_segments(const CUtensorMap* tm_w, const CUtensorMap* tm_x, void* y, const int* seg_start,
+                         const int* seg_end, const int* seg_expert, int G, int max_rows, int N, int K,
+                         unsigned* status, cudaStream_t stream) {
+  if (K % kBK != 0 || N % 8 != 0 || max_rows < 1 || G < 1) return -1;
+  switch (grouped_block_n(max_rows, G)) {
+    case 32: return run_grouped<32>(*tm_w, *tm_x, y, seg_start, seg_end, seg_expert, G, max_rows, N, K, status, stream);
+    case 64: return run_grouped<64>(*tm_w, *tm_x, y, seg_start, seg_end, seg_expert, G, max_rows, N, K, status, stream);
+    default:
+      return run_grouped<128>(*tm_w, *tm_x, y, seg_start, seg_end, seg_expert, G, max_rows, N, K, status, stream);
   }
 }
 

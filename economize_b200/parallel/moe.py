@@ -10,6 +10,13 @@ rank routes its own tokens. Dispatch and combine are all-to-all exchanges of the
 of the per-rank counts, then of the rows and their local expert ids; NCCL on GPUs, Gloo on the CPU); the rows a
 rank receives run through its experts and go back the same way, and the source rank sums each token's weighted
 expert outputs in fp32.
+
+Fused expert parallelism (:class:`FusedExpertParallel`): the same ownership, with the exchanges done by kernels
+(``csrc/ep.cu``) that store the routed rows straight into the peers' IPC-mapped buffers over NVLink and signal with
+system-scope counters. One MoE call is route -> gather -> dispatch -> segments -> grouped gate/up GEMM -> SwiGLU ->
+grouped down GEMM -> combine -> weighted sum, all on the device without a host synchronisation, so expert-parallel
+decode steps record into CUDA graphs. Economize runs MoE models through Hugging Face's blocks only (no expert
+parallelism of its own).
 """
 
 from __future__ import annotations
@@ -19,9 +26,9 @@ import torch.distributed as dist
 import torch.nn.functional as F
 
 from .. import ops
-from ..errors import ConfigError
+from ..errors import CommTimeoutError, ConfigError
 
-__all__ = ["ExpertParallel", "moe_mlp", "moe_reference", "route", "shard_experts"]
+__all__ = ["ExpertParallel", "FusedExpertParallel", "moe_mlp", "moe_reference", "route", "shard_experts"]
 
 
 def route(logits: torch.Tensor, k: int) -> tuple[torch.Tensor, torch.Tensor]:
@@ -138,6 +145,80 @@ class ExpertParallel:
         return out.to(x.dtype).reshape(shape)
 
 
+class FusedExpertParallel(ExpertParallel):
+    """Expert parallelism whose dispatch and combine are peer stores over NVLink (no NCCL call per MoE layer).
+
+    Every rank allocates one symmetric buffer (received rows, their source rows, per-expert counts, returned rows
+    and the arrival counters) and maps every peer's through CUDA IPC; the handles travel once through
+    ``torch.distributed``. Calls with more than ``max_tokens`` tokens use the all-to-all path of
+    :class:`ExpertParallel`, so every rank must see the same side of that bound in a call (lockstep decoding with
+    equal batches does). Ranks must share a node with NVLink peer access.
+
+    Args:
+        rank, size, group: As for :class:`ExpertParallel`.
+        max_tokens: Most tokens one rank routes in one fused call (sizes the buffers: every rank may send all its
+            ``max_tokens * k`` rows to one peer).
+    """
+
+    def __init__(self, rank: int, size: int, group=None, max_tokens: int = 256) -> None:
+        super().__init__(rank, size, group)
+        if size > 8:
+            raise ConfigError("the fused expert-parallel exchange supports up to 8 ranks")
+        self.max_tokens = max_tokens
+        self._ext = None
+        self._own = 0
+        self.ptrs: list[int] = []
+        self._shape: tuple[int, int, int] | None = None
+
+    def setup(self, hidden: int, experts_local: int, k: int) -> None:
+        """Allocate and map the buffers for MoE layers of width ``hidden`` with ``experts_local`` experts per rank
+        and top-``k`` routing (collective: every rank calls it)."""
+        if self._shape == (hidden, experts_local, k):
+            return
+        if self.size * experts_local > 128:
+            raise ConfigError("the fused exchange supports at most 128 (rank, expert) pairs")
+        self.close()
+        ext = ops.require()
+        self._ext = ext
+        self.cap = self.max_tokens * k
+        nbytes = ext.ep_buffer_bytes(self.size, experts_local, self.cap, hidden, self.cap)
+        self._own, handle = ext.symm_alloc(nbytes)
+        handles: list = [None] * self.size
+        dist.all_gather_object(handles, handle, group=self.group)
+        self.ptrs = [self._own if r == self.rank else ext.symm_open(h) for r, h in enumerate(handles)]
+        dist.barrier(group=self.group)
+        self._shape = (hidden, experts_local, k)
+
+    def forward(self, x: torch.Tensor, router: torch.Tensor, w_gate_up: torch.Tensor, w_down: torch.Tensor,
+                k: int) -> torch.Tensor:
+        shape = x.shape
+        x2 = x.reshape(-1, shape[-1]).contiguous()
+        T, H = x2.shape
+        if (not x.is_cuda or T > self.max_tokens or self._shape != (H, w_gate_up.shape[0], k)):
+            return super().forward(x, router, w_gate_up, w_down, k)
+        C = self._ext
+        logits = ops.linear(x2, router)
+        _, weights, pos, offsets = C.moe_route(logits, k)
+        xs = C.moe_gather(x2, pos)
+        out = C.ep_moe(xs, offsets, pos, weights, w_gate_up, w_down, self.ptrs, self.rank, self.cap, self.cap)
+        return out.reshape(shape)
+
+    def check(self) -> None:
+        """Raise :class:`CommTimeoutError` if a bounded wait of this device gave up since the last check."""
+        status = self._ext.status(torch.cuda.current_device()) if self._ext is not None else 0
+        if status & 8:
+            raise CommTimeoutError(f"a peer's expert rows did not arrive in time (status {status})")
+
+    def close(self) -> None:
+        if self._ext is None or not self.ptrs:
+            return
+        for r, p in enumerate(self.ptrs):
+            if r != self.rank:
+                self._ext.symm_close(p)
+        self._ext.symm_free(self._own)
+        self.ptrs, self._shape = [], None
+
+
 def shard_experts(model, ep: ExpertParallel) -> None:
     """Keep this rank's experts in every MoE layer of an engine model and attach ``ep``."""
     with torch.no_grad():
@@ -147,4 +228,6 @@ def shard_experts(model, ep: ExpertParallel) -> None:
             own = ep.owned(layer.router.shape[0])
             layer.w_gate_up = torch.nn.Parameter(layer.w_gate_up.data[own.start:own.stop].contiguous())
             layer.w_down = torch.nn.Parameter(layer.w_down.data[own.start:own.stop].contiguous())
+            if isinstance(ep, FusedExpertParallel) and layer.w_gate_up.is_cuda:
+                ep.setup(layer.w_down.shape[1], len(own), model.config.experts_per_token)
     model.ep = ep

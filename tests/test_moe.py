@@ -141,3 +141,46 @@ def test_moe_model_decodes_on_gpu(cuda):
     p = prompts((20,))[0].to(cuda)
     plain = eff.decode(p, 16, decoding=eco.DecodeConfig(cycle_length=1)).tokens
     assert torch.equal(eff.decode(p, 16).tokens.cpu(), plain.cpu())
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("T,E,k,H,F", [(1, 8, 2, 512, 1024), (61, 8, 2, 1024, 512), (40, 4, 4, 512, 256)])
+def test_fused_ep_single_rank_matches_kernel_path(cuda, T, E, k, H, F):
+    """The peer-store dispatch / segments / combine kernels with one rank (its own buffer as the only peer), over
+    several calls (the arrival counters advance per call) and under CUDA-graph replay."""
+    from economize_b200 import ops
+    from economize_b200.ops._ext import require
+
+    C = require()
+    g = torch.Generator(device=cuda).manual_seed(T)
+    router = (torch.randn(E, H, device=cuda, generator=g) * 0.05).bfloat16()
+    gu = (torch.randn(E, 2 * F, H, device=cuda, generator=g) * 0.02).bfloat16()
+    down = (torch.randn(E, H, F, device=cuda, generator=g) * 0.02).bfloat16()
+    cap = 64 * k
+    own, _ = C.symm_alloc(C.ep_buffer_bytes(1, E, cap, H, cap))
+
+    def fused(x):
+        _, w, pos, off = C.moe_route(ops.linear(x, router), k)
+        return C.ep_moe(C.moe_gather(x, pos), off, pos, w, gu, down, [own], 0, cap, cap)
+
+    try:
+        for n in (T, max(T // 2, 1), T):
+            x = torch.randn(n, H, device=cuda, generator=g).bfloat16()
+            torch.testing.assert_close(fused(x).float(), moe_mlp(x, router, gu, down, k).float(), atol=2e-2, rtol=2e-2)
+        static = torch.randn(T, H, device=cuda, generator=g).bfloat16()
+        fused(static)
+        torch.cuda.synchronize()
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph):
+            out = fused(static)
+        for _ in range(3):
+            static.copy_(torch.randn(T, H, device=cuda, generator=g).bfloat16())
+            graph.replay()
+            torch.testing.assert_close(out.float(), moe_mlp(static, router, gu, down, k).float(), atol=2e-2,
+                                       rtol=2e-2)
+        torch.cuda.synchronize()
+        assert C.status(cuda.index or 0) == 0
+        del graph
+    finally:
+        torch.cuda.synchronize()
+        C.symm_free(own)

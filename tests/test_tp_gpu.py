@@ -107,3 +107,79 @@ def test_tp2_fused_collectives():
                 p.kill()
     for rank, res in results.items():
         assert "error" not in res and all(res.values()), (rank, res)
+
+
+def _ep_worker(rank, world, port, queue):
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), RANK=str(rank), WORLD_SIZE=str(world),
+                      LOCAL_RANK=str(rank), NCCL_NVLS_ENABLE="0")
+    import torch.distributed as dist
+
+    from economize_b200 import ops
+    from economize_b200.distributed import init_distributed
+    from economize_b200.parallel.moe import ExpertParallel, FusedExpertParallel, moe_mlp
+
+    init_distributed("nccl", timeout_s=60)
+    dev = torch.device("cuda", rank)
+    result = {}
+    try:
+        E, k, H, F = 8, 2, 1024, 512
+        g = torch.Generator(device=dev).manual_seed(0)  # same weights on every rank
+        router = (torch.randn(E, H, device=dev, generator=g) * 0.05).bfloat16()
+        gu = (torch.randn(E, 2 * F, H, device=dev, generator=g) * 0.02).bfloat16()
+        down = (torch.randn(E, H, F, device=dev, generator=g) * 0.02).bfloat16()
+        ep = FusedExpertParallel(rank, world, max_tokens=64)
+        own = ep.owned(E)
+        ep.setup(H, len(own), k)
+        lg, ld = gu[own.start:own.stop].contiguous(), down[own.start:own.stop].contiguous()
+        gx = torch.Generator(device=dev).manual_seed(100 + rank)
+        for i, n in enumerate((1 + 7 * rank, 64, 33)):  # ragged token counts across ranks
+            x = torch.randn(n, H, device=dev, generator=gx).bfloat16()
+            out = ep.forward(x, router, lg, ld, k)
+            want = moe_mlp(x, router, gu, down, k)  # all experts on this GPU
+            nccl = ExpertParallel.forward(ep, x, router, lg, ld, k)
+            result[f"fused{i}"] = (out.float() - want.float()).abs().max().item() <= 2e-2
+            result[f"nccl{i}"] = (nccl.float() - want.float()).abs().max().item() <= 3e-2
+        # captured in a CUDA graph (no NCCL call inside) and replayed
+        static = torch.randn(16, H, device=dev, generator=gx).bfloat16()
+        ep.forward(static, router, lg, ld, k)
+        torch.cuda.synchronize()
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph):
+            out = ep.forward(static, router, lg, ld, k)
+        ok = True
+        for _ in range(3):
+            static.copy_(torch.randn(16, H, device=dev, generator=gx).bfloat16())
+            graph.replay()
+            ok = ok and (out.float() - moe_mlp(static, router, gu, down, k).float()).abs().max().item() <= 2e-2
+        result["graph"] = ok
+        torch.cuda.synchronize()
+        del graph
+        ep.check()
+        result["status"] = ops.require().status(rank) == 0
+        dist.barrier()
+        ep.close()
+    except Exception as err:  # report instead of hanging the other rank
+        result["error"] = f"{type(err).__name__}: {err}"
+    torch.cuda.synchronize()
+    queue.put((rank, result))
+    dist.destroy_process_group()
+
+
+def test_ep2_fused_dispatch_combine():
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs 2 GPUs")
+    ctx = mp.get_context("spawn")
+    queue = ctx.Queue()
+    port = _port()
+    procs = [ctx.Process(target=_ep_worker, args=(r, 2, port, queue), daemon=True) for r in range(2)]
+    for p in procs:
+        p.start()
+    try:
+        results = dict(queue.get(timeout=240) for _ in procs)
+    finally:
+        for p in procs:
+            p.join(timeout=30)
+            if p.is_alive():
+                p.kill()
+    for rank, res in results.items():
+        assert "error" not in res and all(res.values()), (rank, res)
