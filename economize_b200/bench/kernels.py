@@ -11,6 +11,8 @@ peaks. Ops:
 * ``gemm_wq``    weight-only int4 / int8 / fp8 GEMM (``--fmt``), vs the bf16 kernel on the same shape
 * ``attention``  tree-masked decode attention over a bf16 slot cache (``--tree`` new tokens per row)
 * ``layer``      one Llama-3.1-8B decoder layer's projections as a CUDA graph (``--tp`` shard), ours vs cuBLAS
+* ``teal``       activation-sparse GEMV (``colsparse_linear`` over a transposed weight) at ``--sparsity`` of the
+  input entries dropped, vs the dense tcgen05 GEMM on the same shape; bytes are the weight rows actually needed
 
 ``--once`` runs a single call without timing (the case a profiler captures).
 """
@@ -150,9 +152,33 @@ def bench_layer(a) -> None:
     _report("layer_projections", {"M": a.m, "tp": tp}, res["ours"], nbytes, flops, res["cublas"])
 
 
+def bench_teal(a) -> None:
+    from .. import ops
+    from ..ops._ext import require
+
+    dev = torch.device("cuda")
+    C = require()
+    x = torch.randn(a.m, a.k, device=dev).bfloat16()
+    t = torch.quantile(x.float().abs().flatten()[:1 << 20], a.sparsity).reshape(()) if a.sparsity > 0 else \
+        torch.zeros((), device=dev)
+    n_copies = 1 if a.once else _copies(2 * a.n * a.k)
+    ws = [(torch.randn(a.n, a.k, device=dev) * 0.02).bfloat16() for _ in range(n_copies)]
+    wts = [w.t().contiguous() for w in ws]
+    if a.once:
+        C.colsparse_linear(x, wts[0], t)
+        torch.cuda.synchronize()
+        return
+    ours = time_graph([lambda wt=wt: C.colsparse_linear(x, wt, t) for wt in wts], a.iters, a.warmup)
+    dense = time_graph([lambda w=w: ops.linear(x, w) for w in ws], a.iters, a.warmup)
+    kept = float((x.abs() > t.bfloat16()).any(0).float().mean())
+    nbytes = 2 * (a.m * a.k + kept * a.n * a.k + a.m * a.n)
+    _report("teal_gemv", {"M": a.m, "N": a.n, "K": a.k, "sparsity": a.sparsity, "rows_kept": round(kept, 3)}, ours,
+            nbytes, 2 * a.m * a.n * a.k * kept, dense)
+
+
 def main(argv: list[str] | None = None) -> None:
     p = argparse.ArgumentParser(description=__doc__.splitlines()[0])
-    p.add_argument("op", choices=["gemm", "gemm_wq", "attention", "layer"])
+    p.add_argument("op", choices=["gemm", "gemm_wq", "attention", "layer", "teal"])
     p.add_argument("--m", type=int, default=61)
     p.add_argument("--n", type=int, default=6144)
     p.add_argument("--k", type=int, default=4096)
@@ -162,11 +188,13 @@ def main(argv: list[str] | None = None) -> None:
     p.add_argument("--tree", type=int, default=61)
     p.add_argument("--ctx", type=int, default=768)
     p.add_argument("--tp", type=int, default=1)
+    p.add_argument("--sparsity", type=float, default=0.5)
     p.add_argument("--iters", type=int, default=20)
     p.add_argument("--warmup", type=int, default=3)
     p.add_argument("--once", action="store_true", help="one untimed call (for profiler captures)")
     a = p.parse_args(argv)
-    {"gemm": bench_gemm, "gemm_wq": bench_gemm_wq, "attention": bench_attention, "layer": bench_layer}[a.op](a)
+    {"gemm": bench_gemm, "gemm_wq": bench_gemm_wq, "attention": bench_attention, "layer": bench_layer,
+     "teal": bench_teal}[a.op](a)
 
 
 if __name__ == "__main__":

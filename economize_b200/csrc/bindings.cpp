@@ -779,6 +779,81 @@ ecz::PeerPtrs peer_ptrs(const std::vector<int64_t>& ptrs) {
   return p;
 }
 
+// ---- activation sparsity (act_sparse.cu) ------------------------------------------------------------------------
+// sparsify(x) @ W^T for x [M <= 16, K] and the transposed weight wt [K, N]: only the rows of wt whose input column
+// some row keeps (|x| > threshold; no threshold: x != 0) are read.
+Tensor colsparse_linear(Tensor x, Tensor wt, c10::optional<Tensor> threshold) {
+  CHECK_CUDA(x);
+  CHECK_BF16(x);
+  CHECK_BF16(wt);
+  TORCH_CHECK(wt.dim() == 2 && wt.is_contiguous() && x.size(-1) == wt.size(0), "colsparse_linear: wt [K, N]");
+  c10::cuda::CUDAGuard guard(x.device());
+  const int K = static_cast<int>(wt.size(0)), N = static_cast<int>(wt.size(1));
+  auto x2 = x.reshape({-1, K}).contiguous();
+  const int M = static_cast<int>(x2.size(0));
+  auto out = at::empty({M, N}, x.options());
+  const float* thr = nullptr;
+  if (threshold.has_value()) {
+    TORCH_CHECK(threshold->scalar_type() == at::kFloat && threshold->numel() == 1 && threshold->is_cuda(),
+                "colsparse_linear: threshold is a CUDA fp32 scalar");
+    thr = threshold->data_ptr<float>();
+  }
+  cudaStream_t stream = at::cuda::getCurrentCUDAStream();
+  const int kc = ecz::colsparse_chunk(M, N, K, num_sms(x.get_device()));
+  const int splits = (K + kc - 1) / kc;
+  Tensor ws;
+  if (splits > 1) ws = at::empty({splits, M, N}, x.options().dtype(at::kFloat));
+  const int rc = ecz::launch_colsparse_gemv(x2.data_ptr(), K, wt.data_ptr(), thr, out.data_ptr(),
+                                            splits > 1 ? ws.data_ptr<float>() : nullptr,
+                                            split_counters(x.device(), stream), M, N, K, kc, stream);
+  TORCH_CHECK(rc == 0, "colsparse_linear: at most 16 rows and N a multiple of 8 (", rc, ")");
+  auto sizes = x.sizes().vec();
+  sizes.back() = N;
+  return out.view(sizes);
+}
+
+// h = (silu(gate) * 1[keep]) * up of a gated MLP over x [M <= 16, H] with w_gate_up [2F, H] (gate rows first), only
+// for kept channels. CATS: gate [M, F] given, keep = |silu(gate)| > threshold. Deja Vu: keep [M, F] (bool) given.
+Tensor glu_rows(Tensor x, Tensor w_gate_up, c10::optional<Tensor> gate, c10::optional<Tensor> keep,
+                c10::optional<Tensor> threshold) {
+  CHECK_CUDA(x);
+  CHECK_BF16(x);
+  CHECK_BF16(w_gate_up);
+  TORCH_CHECK(w_gate_up.dim() == 2 && w_gate_up.is_contiguous() && w_gate_up.size(1) == x.size(-1),
+              "glu_rows: w_gate_up [2F, H]");
+  c10::cuda::CUDAGuard guard(x.device());
+  const int H = static_cast<int>(w_gate_up.size(1)), F = static_cast<int>(w_gate_up.size(0) / 2);
+  auto x2 = x.reshape({-1, H}).contiguous();
+  const int M = static_cast<int>(x2.size(0));
+  auto h = at::empty({M, F}, x.options());
+  const void* g = nullptr;
+  int ld_gate = F;
+  Tensor g2, k2;
+  const uint8_t* kp = nullptr;
+  if (keep.has_value()) {
+    TORCH_CHECK(keep->numel() == static_cast<int64_t>(M) * F, "glu_rows: keep [M, F]");
+    k2 = keep->reshape({M, F}).to(at::kByte).contiguous();
+    kp = k2.data_ptr<uint8_t>();
+  } else {
+    TORCH_CHECK(gate.has_value() && threshold.has_value(), "glu_rows: CATS needs the gate output and a threshold");
+    CHECK_BF16((*gate));
+    g2 = gate->reshape({M, F}).contiguous();
+    g = g2.data_ptr();
+  }
+  const float* thr = nullptr;
+  if (threshold.has_value()) {
+    TORCH_CHECK(threshold->scalar_type() == at::kFloat && threshold->numel() == 1 && threshold->is_cuda(),
+                "glu_rows: threshold is a CUDA fp32 scalar");
+    thr = threshold->data_ptr<float>();
+  }
+  const int rc = ecz::launch_glu_rows(x2.data_ptr(), H, w_gate_up.data_ptr(), g, ld_gate, kp, thr, h.data_ptr(), M, F,
+                                      H, at::cuda::getCurrentCUDAStream());
+  TORCH_CHECK(rc == 0, "glu_rows: at most 16 rows and H a multiple of 8");
+  auto sizes = x.sizes().vec();
+  sizes.back() = F;
+  return h.view(sizes);
+}
+
 // ---- expert parallelism over NVLink peer memory (ep.cu) ---------------------------------------------------------
 int64_t ep_buffer_bytes(int64_t world, int64_t experts_local, int64_t cap, int64_t hidden, int64_t ret_rows) {
   return ecz::ep_layout(static_cast<int>(world), static_cast<int>(experts_local), static_cast<int>(cap),
@@ -966,6 +1041,8 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("sample", &sample, "inverse-CDF draw of one token per probability row");
   m.def("rejection", &rejection, "lossless speculative sampling of a draft chain (accept/reject + resample)");
   m.def("ngram", &ngram, "prompt-lookup draft proposals from the token history");
+  m.def("colsparse_linear", &colsparse_linear, "activation-sparse GEMV over a transposed weight (<= 16 rows)");
+  m.def("glu_rows", &glu_rows, "gated-MLP hidden over the kept channels only (CATS / Deja Vu, <= 16 rows)");
   m.def("ep_buffer_bytes", &ep_buffer_bytes, "bytes of one rank's expert-parallel symmetric buffer");
   m.def("ep_moe", &ep_moe, "expert-parallel MoE MLP with NVLink peer-store dispatch and combine");
   m.def("symm_alloc", &symm_alloc, "cudaMalloc an IPC-exportable buffer: (pointer, handle)");

@@ -27,6 +27,7 @@ from .. import ops
 from ..errors import ConfigError
 from ..models.llama import CausalLM
 from ..runtime.cache import KVCache, StepBatch
+from ..runtime.phase import phase
 from .config import DecodeConfig
 from .drafter import DraftModel
 from .policies import POLICIES, ConfidencePolicy, DynamicTreePolicy
@@ -221,10 +222,11 @@ class SpecEngine:
         capture = drafter.capture_layers if drafter is not None else ()
         chunk = self.config.prefill_chunk
         model.begin_sequence(st.cache)
-        if chunk is not None and width > chunk:
-            hidden, aux = self._chunked_prefill(st, prompts, lengths, chunk, capture)
-        else:
-            hidden, aux = model.forward_step(prompts, StepBatch.prefill(lengths, width), st.cache, capture)
+        with phase("prefill"):
+            if chunk is not None and width > chunk:
+                hidden, aux = self._chunked_prefill(st, prompts, lengths, chunk, capture)
+            else:
+                hidden, aux = model.forward_step(prompts, StepBatch.prefill(lengths, width), st.cache, capture)
         last_idx = (lengths.long() - 1).clamp_min(0)
         rows = torch.arange(batch, device=prompts.device)
         bonus = self._pred(hidden[rows, last_idx])
@@ -244,7 +246,9 @@ class SpecEngine:
             tokens[rows, lengths.long()] = bonus
             sources = torch.cat([torch.zeros_like(fused[:, :1]), fused], 1)
             n_valid = lengths + 1
-            root_logits, root_state = drafter.observe(tokens, sources, torch.zeros_like(lengths), n_valid, lengths)
+            with phase("draft"):
+                root_logits, root_state = drafter.observe(tokens, sources, torch.zeros_like(lengths), n_valid,
+                                                          lengths)
             if root_logits is not None:
                 st.root_logits.copy_(root_logits)
                 st.root_state.copy_(root_state)
@@ -321,7 +325,8 @@ class SpecEngine:
         one = torch.ones(batch, dtype=torch.int32, device=st.kv_len.device)
         sb = StepBatch(st.kv_len, one, st.kv_len[:, None].contiguous(),
                        torch.ones(batch, 1, dtype=torch.int64, device=st.kv_len.device))
-        hidden, _ = model.forward_step(st.last[:, None], sb, st.cache)
+        with phase("decode"):
+            hidden, _ = model.forward_step(st.last[:, None], sb, st.cache)
         pred = self._pred(hidden[:, 0])
         active = st.n_out < st.max_new
         st.out.scatter_(1, torch.where(active, st.n_out, st.out_cap).long()[:, None], pred[:, None])
@@ -335,12 +340,13 @@ class SpecEngine:
         batch, dev = st.batch, st.kv_len.device
         depth = self.depth
         q_full = None
-        if self.static:
-            draft_tokens, draft_parents = drafter.propose(st.history, st.kv_len + 1)
-        elif self.tree is not None:
-            draft_tokens, draft_parents = self._draft_tree(st)
-        else:
-            draft_tokens, draft_parents, q_full = self._draft_chain(st)
+        with phase("draft"):
+            if self.static:
+                draft_tokens, draft_parents = drafter.propose(st.history, st.kv_len + 1)
+            elif self.tree is not None:
+                draft_tokens, draft_parents = self._draft_tree(st)
+            else:
+                draft_tokens, draft_parents, q_full = self._draft_chain(st)
         # ---- verify: root + drafts in one tree pass ----
         tokens = torch.cat([st.last[:, None], draft_tokens], 1)  # [B, T]
         length = tokens.shape[1]
@@ -349,7 +355,8 @@ class SpecEngine:
         positions = (st.kv_len[:, None] + (popcount64(bits) - 1)).to(torch.int32)
         n_new = torch.full((batch,), length, dtype=torch.int32, device=dev)
         sb = StepBatch(st.kv_len, n_new, positions, bits)
-        hidden, aux = model.forward_step(tokens.clamp_min(0), sb, st.cache, drafter.capture_layers)
+        with phase("refresh"):
+            hidden, aux = model.forward_step(tokens.clamp_min(0), sb, st.cache, drafter.capture_layers)
         n_acc, path, out = self._verify(tokens, parents, hidden, draft_tokens, q_full)
         ops.kv_compact(st.cache.data, st.kv_len, path, n_acc)
         # ---- commit ----
@@ -377,7 +384,8 @@ class SpecEngine:
         obs_tokens = torch.cat([st.last[:, None], out[:, :width]], 1)  # [B, D+2]
         sources = torch.cat([st.carry[:, None].to(fused.dtype), fused], 1)
         n_valid = (n_acc + 2).to(torch.int32)
-        root_logits, root_state = drafter.observe(obs_tokens, sources, st.kv_len, n_valid, n_valid - 1)
+        with phase("draft"):
+            root_logits, root_state = drafter.observe(obs_tokens, sources, st.kv_len, n_valid, n_valid - 1)
         st.carry.copy_(fused[rows, n_acc.long()])
         st.last.copy_(out[rows, n_acc.long()])
         st.kv_len.add_(n_acc + 1)

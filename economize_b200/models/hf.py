@@ -69,7 +69,9 @@ def export_hf_state(model, copy: bool = True) -> dict[str, torch.Tensor]:
     c = model.config
 
     def full(t):
-        return t.dequantize() if isinstance(t, QWeight) else t.detach()
+        if isinstance(t, QWeight) or (not isinstance(t, torch.Tensor) and hasattr(t, "dequantize")):
+            return t.dequantize()
+        return t.detach()
 
     out = {"model.embed_tokens.weight": model.embed.detach(), "model.norm.weight": model.norm.detach()}
     if model.lm_head is not None:

@@ -130,14 +130,15 @@ class CausalLM(nn.Module):
         return self.embed[tokens]
 
     def forward_step(self, tokens: torch.Tensor, batch: StepBatch, cache: KVCache,
-                     capture: tuple[int, ...] = (), layers: range | None = None,
+                     capture: tuple[int, ...] = (), layers: range | None = None, hidden: torch.Tensor | None = None,
                      ) -> tuple[torch.Tensor, dict[int, torch.Tensor]]:
         """Run a pass over ``tokens [B, T]``; returns the final-normed hidden states ``[B, T, H]`` and the captured
         block outputs ``{i: [B, T, H]}`` (``0``: the embeddings, ``i``: the output of ``i`` blocks, ``-1``: the
-        final-normed states again)."""
+        final-normed states again, ``-2``: the residual stream after the last block that ran). ``hidden`` replaces
+        the embeddings as the input of the first block that runs (with ``layers``: one block on given inputs)."""
         c = self.config
         cos, sin = self.rope_tables()
-        h = self.embed_tokens(tokens)
+        h = self.embed_tokens(tokens) if hidden is None else hidden
         resid: torch.Tensor | None = None
         aux: dict[int, torch.Tensor] = {}
         todo = layers if layers is not None else range(c.num_layers)
@@ -162,6 +163,8 @@ class CausalLM(nn.Module):
             aux[c.num_layers] = resid
         if -1 in capture:  # the final-normed hidden states (what the LM head reads)
             aux[-1] = out
+        if -2 in capture:
+            aux[-2] = resid
         return out, aux
 
     def _norm(self, h: torch.Tensor, weight: torch.Tensor, resid: torch.Tensor | None,
@@ -183,6 +186,9 @@ class CausalLM(nn.Module):
         c = self.config
         if self.observer is not None:
             self.observer(index, "wqkv", x)
+        hook = getattr(layer, "attn_input_hook", None)  # Deja Vu's lookahead predictors read the attention input
+        if hook is not None:
+            hook(x)
         qkv = self._linear(x, layer.wqkv) if layer.bqkv is None else ops.linear(x, layer.wqkv, layer.bqkv)
         k_cache, v_cache = cache.layer(index)
         k_scale, v_scale = cache.layer_scales(index)
@@ -226,6 +232,11 @@ class CausalLM(nn.Module):
                            getattr(self, "ep", None))
         if self.observer is not None:
             self.observer(index, "w_gate_up", x)
+        rule = getattr(layer, "mlp_rule", None)  # activation-sparse MLPs (CATS, Deja Vu); None: the dense path
+        if rule is not None:
+            out = rule(self, layer, x, index)
+            if out is not None:
+                return out
         a = ops.silu_mul(self._linear(x, layer.w_gate_up))
         if self.observer is not None:
             self.observer(index, "w_down", a)
