@@ -13,6 +13,8 @@ peaks. Ops:
 * ``layer``      one Llama-3.1-8B decoder layer's projections as a CUDA graph (``--tp`` shard), ours vs cuBLAS
 * ``teal``       activation-sparse GEMV (``colsparse_linear`` over a transposed weight) at ``--sparsity`` of the
   input entries dropped, vs the dense tcgen05 GEMM on the same shape; bytes are the weight rows actually needed
+* ``glu``        CATS's gated rows (``glu_rows``: up rows of the channels with ``|silu(gate)| > t``, ``--n`` = FFN
+  width, ``--k`` = hidden) at ``--sparsity``, vs the dense up projection GEMM
 
 ``--once`` runs a single call without timing (the case a profiler captures).
 """
@@ -176,9 +178,35 @@ def bench_teal(a) -> None:
             nbytes, 2 * a.m * a.n * a.k * kept, dense)
 
 
+def bench_glu(a) -> None:
+    from .. import ops
+    from ..ops._ext import require
+
+    dev = torch.device("cuda")
+    C = require()
+    F_, H = a.n, a.k
+    x = torch.randn(a.m, H, device=dev).bfloat16()
+    n_copies = 1 if a.once else _copies(4 * F_ * H)
+    ws = [(torch.randn(2 * F_, H, device=dev) * 0.02).bfloat16() for _ in range(n_copies)]
+    gates = [ops.linear(x, w[:F_]) for w in ws]
+    s = torch.nn.functional.silu(gates[0].float()).abs().flatten()
+    t = torch.quantile(s, a.sparsity).reshape(()) if a.sparsity > 0 else torch.zeros((), device=dev)
+    if a.once:
+        C.glu_rows(x, ws[0], gates[0], None, t)
+        torch.cuda.synchronize()
+        return
+    ours = time_graph([lambda w=w, g=g: C.glu_rows(x, w, g, None, t) for w, g in zip(ws, gates)], a.iters, a.warmup)
+    ups = [w[F_:] for w in ws]
+    dense = time_graph([lambda u=u: ops.linear(x, u) for u in ups], a.iters, a.warmup)
+    kept = float((torch.nn.functional.silu(gates[0].float()).abs() > t).any(0).float().mean())
+    nbytes = 2 * (a.m * H + kept * F_ * H + 2 * a.m * F_)
+    _report("cats_glu_rows", {"M": a.m, "F": F_, "H": H, "sparsity": a.sparsity, "rows_kept": round(kept, 3)}, ours,
+            nbytes, 2 * a.m * F_ * H * kept, dense)
+
+
 def main(argv: list[str] | None = None) -> None:
     p = argparse.ArgumentParser(description=__doc__.splitlines()[0])
-    p.add_argument("op", choices=["gemm", "gemm_wq", "attention", "layer", "teal"])
+    p.add_argument("op", choices=["gemm", "gemm_wq", "attention", "layer", "teal", "glu"])
     p.add_argument("--m", type=int, default=61)
     p.add_argument("--n", type=int, default=6144)
     p.add_argument("--k", type=int, default=4096)
@@ -194,7 +222,7 @@ def main(argv: list[str] | None = None) -> None:
     p.add_argument("--once", action="store_true", help="one untimed call (for profiler captures)")
     a = p.parse_args(argv)
     {"gemm": bench_gemm, "gemm_wq": bench_gemm_wq, "attention": bench_attention, "layer": bench_layer,
-     "teal": bench_teal}[a.op](a)
+     "teal": bench_teal, "glu": bench_glu}[a.op](a)
 
 
 if __name__ == "__main__":

@@ -4,10 +4,11 @@
 //   colsparse_gemv_kernel  y = sparsify(x) @ W^T with W stored transposed (W^T [K, N], row-major): only the rows
 //                          k of W^T whose input column is kept by some row of x are streamed (TEAL: |x| > t; with
 //                          t = 0 the exact zeros of a CATS / Deja Vu down-projection input are skipped).
-//                          Each CTA compacts the kept columns of 128-wide chunks of its K range into shared memory;
-//                          every quarter-warp then streams one 128-byte segment of a kept W^T row (8 lanes x 16 B)
-//                          so one warp has eight rows of 64 columns in flight per step. Split-K partials are summed
-//                          in split order by the last CTA of each column tile (deterministic).
+//                          Each CTA compacts the kept columns of its K range chunk by chunk into shared memory;
+//                          every quarter-warp then streams one 128-byte segment of a kept W^T row (8 lanes x 16 B),
+//                          eight rows in flight. K-groups of warps split each chunk and are summed in shared memory;
+//                          the split-K partials of a column tile are summed in split order by its last CTA, so the
+//                          result is deterministic.
 //   glu_rows_kernel        h = (g * 1[keep]) * up(x) of a gated MLP whose [gate; up] weight is row-major [2F, H]:
 //                          only the up rows (CATS: gate given densely, keep = |silu(gate)| > t) or the gate and up
 //                          rows (Deja Vu: keep given by the predictor) of kept channels are read.
@@ -46,11 +47,15 @@ __device__ __forceinline__ float threshold_of(const float* thr) {
   return thr != nullptr ? __bfloat162float(__float2bfloat16(*thr)) : 0.f;
 }
 
-constexpr int kCsChunk = 128;   // K columns compacted per step (= threads of the CTA)
-constexpr int kCsTile = 256;    // output columns per CTA (4 warps x 64)
+constexpr int kCsTile = 256;   // output columns per CTA (4 warps x 64)
+constexpr int kCsChunk = 128;  // K columns compacted per step (one per thread)
+constexpr int kCsCluster = 8;  // CTAs of one column tile whose partials are summed through DSMEM
 
+// grid (column tiles, CS * G), cluster (1, CS): CTA (tile, split) streams the kept rows of its K range; the CS
+// CTAs of a cluster sum their partial tiles through distributed shared memory in rank order, and with G > 1 the
+// tile's last cluster sums the G cluster partials in order (deterministic; no fp32 atomics).
 template <int MT>
-__global__ void __launch_bounds__(128) colsparse_gemv_kernel(const bf16* __restrict__ x, int ldx,
+__global__ void __launch_bounds__(128, MT <= 4 ? 8 : 2) colsparse_gemv_kernel(const bf16* __restrict__ x, int ldx,
                                                              const bf16* __restrict__ wt, const float* thr,
                                                              bf16* __restrict__ out, float* __restrict__ ws,
                                                              int* __restrict__ counters, int M, int N, int K, int kc) {
@@ -58,6 +63,7 @@ __global__ void __launch_bounds__(128) colsparse_gemv_kernel(const bf16* __restr
   pdl_wait();
   __shared__ int act_k[kCsChunk];
   __shared__ float act_x[MT][kCsChunk];
+  __shared__ __align__(16) float part[MT][kCsTile];
   __shared__ int warp_cnt[4];
   __shared__ int is_last;
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
@@ -65,7 +71,7 @@ __global__ void __launch_bounds__(128) colsparse_gemv_kernel(const bf16* __restr
   const int q = lane >> 3;                                            // which kept row of each group of 4
   const bool col_ok = n0 < N;
   const int split = blockIdx.y;
-  const int k_begin = split * kc, k_end = min(K, k_begin + kc);
+  const int k_begin = min(K, split * kc), k_end = min(K, k_begin + kc);
   const float t = threshold_of(thr);
   float acc[MT][8];
 #pragma unroll
@@ -134,7 +140,7 @@ __global__ void __launch_bounds__(128) colsparse_gemv_kernel(const bf16* __restr
     }
     __syncthreads();  // the next chunk overwrites act_k / act_x
   }
-  // ---- sum the four quarter-warps (fixed order: deterministic) ----
+  // ---- sum the four quarter-warps (fixed order) into this CTA's partial tile ----
 #pragma unroll
   for (int m = 0; m < MT; ++m)
 #pragma unroll
@@ -142,47 +148,77 @@ __global__ void __launch_bounds__(128) colsparse_gemv_kernel(const bf16* __restr
       acc[m][c] += __shfl_xor_sync(0xffffffffu, acc[m][c], 8);
       acc[m][c] += __shfl_xor_sync(0xffffffffu, acc[m][c], 16);
     }
-  if (gridDim.y == 1) {
-    if (q == 0 && col_ok) {
-#pragma unroll
-      for (int m = 0; m < MT; ++m) {
-        if (m >= M) break;
-        uint4 o;
-        __nv_bfloat162* h = reinterpret_cast<__nv_bfloat162*>(&o);
-#pragma unroll
-        for (int i = 0; i < 4; ++i) h[i] = __floats2bfloat162_rn(acc[m][2 * i], acc[m][2 * i + 1]);
-        *reinterpret_cast<uint4*>(out + static_cast<long>(m) * N + n0) = o;
-      }
-    }
-    return;
-  }
-  if (q == 0 && col_ok) {
+  if (q == 0) {
+    const int cin = warp * 64 + (lane & 7) * 8;
 #pragma unroll
     for (int m = 0; m < MT; ++m) {
-      if (m >= M) break;
-      float4* dst = reinterpret_cast<float4*>(ws + (static_cast<long>(split) * M + m) * N + n0);
+      float4* dst = reinterpret_cast<float4*>(&part[m][cin]);
       dst[0] = make_float4(acc[m][0], acc[m][1], acc[m][2], acc[m][3]);
       dst[1] = make_float4(acc[m][4], acc[m][5], acc[m][6], acc[m][7]);
     }
   }
+  // ---- cluster: rank r sums columns [r * 256 / CS, (r + 1) * 256 / CS) over the CS CTAs in rank order ----
+  const int CS = min(static_cast<int>(gridDim.y), kCsCluster);
+  const int G = gridDim.y / CS;
+  const int rank = static_cast<int>(cluster_ctarank());
+  cluster_sync();
+  const int span = (kCsTile / CS) & ~3;  // 16-byte aligned slices; the last rank also takes the remainder
+  const int c_lo = rank * span, c_hi = rank == CS - 1 ? kCsTile : c_lo + span;
+  const int g = split / CS;
+  for (int i = tid; i < M * ((c_hi - c_lo + 3) / 4); i += 128) {
+    const int per = (c_hi - c_lo + 3) / 4;
+    const int m = i / per, c = c_lo + (i % per) * 4;
+    float4 sum = make_float4(0.f, 0.f, 0.f, 0.f);
+    const uint32_t local = static_cast<uint32_t>(__cvta_generic_to_shared(&part[m][c]));
+    for (int r = 0; r < CS; ++r) {
+      const float4 v = ld_dsmem_v4(local, r);
+      sum.x += v.x;
+      sum.y += v.y;
+      sum.z += v.z;
+      sum.w += v.w;
+    }
+    const int col = blockIdx.x * kCsTile + c;
+    if (col >= N) continue;
+    if (G == 1) {
+      __nv_bfloat162* o = reinterpret_cast<__nv_bfloat162*>(out + static_cast<long>(m) * N + col);
+      o[0] = __floats2bfloat162_rn(sum.x, sum.y);
+      o[1] = __floats2bfloat162_rn(sum.z, sum.w);
+    } else {
+      *reinterpret_cast<float4*>(ws + (static_cast<long>(g) * M + m) * N + col) = sum;
+    }
+  }
+  cluster_sync();  // the peers' partial tiles stay alive until every rank has read them
+  if (G == 1) return;
   __threadfence();
   __syncthreads();
   if (tid == 0) is_last = atomicAdd(&counters[blockIdx.x], 1) == static_cast<int>(gridDim.y) - 1;
   __syncthreads();
   if (!is_last) return;
   __threadfence();
-  // the last CTA of this column tile: out = sum of the splits' partials in split order
-  const int col = blockIdx.x * kCsTile + tid * 2;
-  if (col < N) {
-    for (int m = 0; m < M; ++m) {
-      float2 s = make_float2(0.f, 0.f);
-      for (int sp = 0; sp < static_cast<int>(gridDim.y); ++sp) {
-        const float2 v = __ldcg(reinterpret_cast<const float2*>(ws + (static_cast<long>(sp) * M + m) * N + col));
-        s.x += v.x;
-        s.y += v.y;
-      }
-      *reinterpret_cast<__nv_bfloat162*>(out + static_cast<long>(m) * N + col) = __floats2bfloat162_rn(s.x, s.y);
+  // the tile's last CTA: out = sum of the G cluster partials in order (all loads in flight at once)
+  for (int i = tid; i < M * (kCsTile / 4); i += 128) {
+    const int m = i / (kCsTile / 4), c = (i % (kCsTile / 4)) * 4;
+    const int col = blockIdx.x * kCsTile + c;
+    if (col >= N) continue;
+    float4 sum = make_float4(0.f, 0.f, 0.f, 0.f);
+    for (int g0 = 0; g0 < G; g0 += 8) {  // eight cluster partials in flight
+      float4 v[8];
+#pragma unroll
+      for (int u = 0; u < 8; ++u)
+        if (g0 + u < G)
+          v[u] = __ldcg(reinterpret_cast<const float4*>(ws + (static_cast<long>(g0 + u) * M + m) * N + col));
+#pragma unroll
+      for (int u = 0; u < 8; ++u)
+        if (g0 + u < G) {
+          sum.x += v[u].x;
+          sum.y += v[u].y;
+          sum.z += v[u].z;
+          sum.w += v[u].w;
+        }
     }
+    __nv_bfloat162* o = reinterpret_cast<__nv_bfloat162*>(out + static_cast<long>(m) * N + col);
+    o[0] = __floats2bfloat162_rn(sum.x, sum.y);
+    o[1] = __floats2bfloat162_rn(sum.z, sum.w);
   }
   if (tid == 0) counters[blockIdx.x] = 0;
 }
@@ -318,8 +354,21 @@ __global__ void __launch_bounds__(128) glu_rows_kernel(const bf16* __restrict__ 
 template <int MT>
 void run_colsparse(const bf16* x, int ldx, const bf16* wt, const float* thr, bf16* out, float* ws, int* counters,
                    int M, int N, int K, int splits, int kc, cudaStream_t stream) {
-  const dim3 grid((N + kCsTile - 1) / kCsTile, splits);
-  launch_pdl(colsparse_gemv_kernel<MT>, grid, dim3(128), 0, stream, x, ldx, wt, thr, out, ws, counters, M, N, K, kc);
+  const int cs = std::min(splits, kCsCluster);
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3((N + kCsTile - 1) / kCsTile, splits);
+  cfg.blockDim = dim3(128);
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[2];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = pdl_enabled() ? 1 : 0;
+  attr[1].id = cudaLaunchAttributeClusterDimension;
+  attr[1].val.clusterDim.x = 1;
+  attr[1].val.clusterDim.y = cs;
+  attr[1].val.clusterDim.z = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 2;
+  cudaLaunchKernelEx(&cfg, colsparse_gemv_kernel<MT>, x, ldx, wt, thr, out, ws, counters, M, N, K, kc);
 }
 
 template <int MT>
@@ -337,20 +386,24 @@ void run_glu(const bf16* x, int ldx, const bf16* w, const bf16* gate_pre, int ld
 
 }  // namespace
 
-// K chunk per CTA (a multiple of 128) for about 8 CTAs per SM; the split count is ceil(K / chunk).
-int colsparse_chunk(int M, int N, int K, int num_sms) {
+// Split count: about 8 CTAs per SM in one wave, as CS CTAs per cluster (CS <= 8) times G <= 16 cluster groups; the
+// K range per CTA is a multiple of 128 (CTAs past the end of K contribute zeros).
+int colsparse_splits(int M, int N, int K, int num_sms) {
   const int tiles = (N + kCsTile - 1) / kCsTile;
   const int target = num_sms * (M <= 4 ? 8 : 4);
-  const int splits = std::max(1, std::min((target + tiles - 1) / tiles, (K + kCsChunk - 1) / kCsChunk));
-  const int kc = (K + splits - 1) / splits;
-  return (kc + kCsChunk - 1) / kCsChunk * kCsChunk;
+  int want = std::max(1, std::min((target + tiles - 1) / tiles, (K + kCsChunk - 1) / kCsChunk));
+  if (want <= kCsCluster) return want;
+  const int groups = std::min(16, (want + kCsCluster - 1) / kCsCluster);
+  return groups * kCsCluster;
 }
 
 int launch_colsparse_gemv(const void* x, int ldx, const void* wt, const float* thr, void* out, float* ws,
-                          int* counters, int M, int N, int K, int kc, cudaStream_t stream) {
-  if (M < 1 || M > 16 || N % 8 != 0 || kc % kCsChunk != 0 || (N + kCsTile - 1) / kCsTile > 8192) return -1;
-  const int splits = (K + kc - 1) / kc;
-  if (splits > 1 && (ws == nullptr || counters == nullptr)) return -2;
+                          int* counters, int M, int N, int K, int splits, cudaStream_t stream) {
+  if (M < 1 || M > 16 || N % 8 != 0 || splits < 1 || (N + kCsTile - 1) / kCsTile > 8192) return -1;
+  if (splits > kCsCluster && (splits % kCsCluster != 0 || splits / kCsCluster > 16)) return -1;
+  if (splits > kCsCluster && (ws == nullptr || counters == nullptr)) return -2;
+  int kc = (K + splits - 1) / splits;
+  kc = (kc + kCsChunk - 1) / kCsChunk * kCsChunk;
   auto xb = static_cast<const bf16*>(x);
   auto wb = static_cast<const bf16*>(wt);
   auto ob = static_cast<bf16*>(out);

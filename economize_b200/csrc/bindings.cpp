@@ -799,13 +799,12 @@ Tensor colsparse_linear(Tensor x, Tensor wt, c10::optional<Tensor> threshold) {
     thr = threshold->data_ptr<float>();
   }
   cudaStream_t stream = at::cuda::getCurrentCUDAStream();
-  const int kc = ecz::colsparse_chunk(M, N, K, num_sms(x.get_device()));
-  const int splits = (K + kc - 1) / kc;
+  const int splits = ecz::colsparse_splits(M, N, K, num_sms(x.get_device()));
   Tensor ws;
-  if (splits > 1) ws = at::empty({splits, M, N}, x.options().dtype(at::kFloat));
+  if (splits > 8) ws = at::empty({splits / 8, M, N}, x.options().dtype(at::kFloat));
   const int rc = ecz::launch_colsparse_gemv(x2.data_ptr(), K, wt.data_ptr(), thr, out.data_ptr(),
-                                            splits > 1 ? ws.data_ptr<float>() : nullptr,
-                                            split_counters(x.device(), stream), M, N, K, kc, stream);
+                                            splits > 8 ? ws.data_ptr<float>() : nullptr,
+                                            split_counters(x.device(), stream), M, N, K, splits, stream);
   TORCH_CHECK(rc == 0, "colsparse_linear: at most 16 rows and N a multiple of 8 (", rc, ")");
   auto sizes = x.sizes().vec();
   sizes.back() = N;

@@ -143,11 +143,12 @@ int launch_gemm_segments(const CUtensorMap* tm_w, const CUtensorMap* tm_x, void*
                          const int* seg_end, const int* seg_expert, int G, int max_rows, int N, int K,
                          unsigned* status, cudaStream_t stream);
 
-// act_sparse.cu: activation-sparse GEMVs (<= 16 rows). ws: ceil(K / kc) * M * N floats; counters: zeroed, one
-// per 256 output columns, private to the stream (reset by the kernel).
-int colsparse_chunk(int M, int N, int K, int num_sms);
+// act_sparse.cu: activation-sparse GEMVs (<= 16 rows). splits = colsparse_splits(...); with splits > 8, ws holds
+// (splits / 8) * M * N floats and counters (zeroed, one per 256 output columns, private to the stream) are reset by
+// the kernel.
+int colsparse_splits(int M, int N, int K, int num_sms);
 int launch_colsparse_gemv(const void* x, int ldx, const void* wt, const float* thr, void* out, float* ws,
-                          int* counters, int M, int N, int K, int kc, cudaStream_t stream);
+                          int* counters, int M, int N, int K, int splits, cudaStream_t stream);
 int launch_glu_rows(const void* x, int ldx, const void* w, const void* gate_pre, int ld_gate, const uint8_t* keep,
                     const float* thr, void* h, int M, int F, int H, cudaStream_t stream);
 

@@ -29,8 +29,9 @@ __all__ = ["MAX_ROWS", "PREFILL_MODES", "GreedyStep", "PhasePolicy", "TealWeight
            "apply_mode", "block_sparsity", "cats_mlp", "greedy_allocation", "greedy_error", "kept_channels",
            "kept_mlp", "magnitude_quantile", "sparsify", "topk_mask", "uniform_allocation"]
 
-#: Most rows (tokens x sequences) a call may have to run the sparse kernels; more rows keep nearly every column.
-MAX_ROWS = 16
+#: Most rows (tokens x sequences) a call may have to run the sparse kernels: from about four independent rows on,
+#: their union keeps nearly every column and the dense GEMM is faster.
+MAX_ROWS = 4
 
 #: How a forward call's tokens are treated: ``"dense"`` unchanged, ``"second_half"`` the last ``max(1, S // 2)``
 #: positions of every sequence are sparsified (TEAL's perplexity protocol), ``"all"`` every position.
