@@ -347,6 +347,10 @@ class SpecEngine:
                 draft_tokens, draft_parents = self._draft_tree(st)
             else:
                 draft_tokens, draft_parents, q_full = self._draft_chain(st)
+            overlay = getattr(drafter, "overlay", None)  # a hybrid lays its primary's proposals over the drafts
+            if overlay is not None:
+                draft_tokens, draft_parents, q_full = overlay(st.history, st.kv_len + 1, draft_tokens, draft_parents,
+                                                              q_full)
         # ---- verify: root + drafts in one tree pass ----
         tokens = torch.cat([st.last[:, None], draft_tokens], 1)  # [B, T]
         length = tokens.shape[1]
@@ -467,7 +471,7 @@ class SpecEngine:
             k = drafts.shape[1]
             n_acc, out = ops.rejection(p, q_full.contiguous(), drafts.clamp_min(0),
                                        torch.rand(batch, k, device=dev), torch.rand(batch, device=dev))
-            if self.min_confidence is not None:  # invalidated drafts are never kept
+            if self.min_confidence is not None or hasattr(self.drafter, "overlay"):  # invalid drafts never kept
                 limit = (drafts >= 0).int().cumprod(1).sum(1).to(torch.int32)
                 n_acc = torch.minimum(n_acc, limit)
             path = torch.arange(length, device=dev, dtype=torch.int32).expand(batch, length)

@@ -40,6 +40,13 @@ class LayerRef(nn.Module):
         except AttributeError:
             return getattr(self.__dict__["_target"][0], name)
 
+    def register_parameter(self, name: str, param: nn.Parameter | None) -> None:
+        """A parameter of the view's own that shadows the target's (a draft path's rewritten weight); the base
+        class would refuse it because the name resolves to the target's attribute."""
+        if param is not None and not isinstance(param, nn.Parameter):
+            raise TypeError(f"cannot assign {type(param).__name__} as parameter {name!r}")
+        self._parameters[name] = param
+
 
 def layer_view(target: CausalLM, layers: Sequence[int | tuple[int, bool, bool]],
                extra: Sequence[nn.Module] = ()) -> CausalLM:

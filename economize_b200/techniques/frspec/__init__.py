@@ -51,6 +51,8 @@ class FRSpecTechnique(Technique):
 
     def after_drafter(self, technique: nn.Module) -> None:
         """Restrict ``technique``'s head (called once the drafter is attached)."""
+        while hasattr(technique, "wrapped_drafter"):  # a hybrid's fallback
+            technique = technique.wrapped_drafter
         if technique.name != "eagle3":
             raise ConfigError(f"frspec restricts an eagle3 draft head, not {technique.name}")
         if self.token_ids.numel() == 0:

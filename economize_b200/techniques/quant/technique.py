@@ -235,6 +235,8 @@ class DraftQuantTechnique(_QuantBase):
     @torch.no_grad()
     def after_drafter(self, technique: nn.Module) -> None:
         cfg: DraftQuantConfig = self.config
+        while hasattr(technique, "wrapped_drafter"):  # a hybrid's fallback
+            technique = technique.wrapped_drafter
         if not self.weights:
             for name, p in list(technique.named_parameters()):
                 if p.dim() != 2 or not _selected((name,), cfg.targets, cfg.exclude):
