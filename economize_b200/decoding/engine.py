@@ -213,6 +213,8 @@ class SpecEngine:
             st.cycles.zero_()
         if self.drafter is not None:
             self.drafter.begin(batch, capacity)
+            if hasattr(self.drafter, "bind_target_cache"):  # drafters that run target layers (Hidden Transfer)
+                self.drafter.bind_target_cache(st.cache)
         return st
 
     # ---- prefill -----------------------------------------------------------------------------------------------
@@ -413,7 +415,13 @@ class SpecEngine:
             q_full[:, ids] = q
             return tok, q_full, q.gather(1, d[:, None])[:, 0]
         d = ops.argmax(logits)
-        top = torch.softmax(logits.float(), -1).gather(1, d[:, None])[:, 0] if self.min_confidence else logits[:, 0]
+        if not self.min_confidence:
+            top = logits[:, 0]
+        elif getattr(drafter, "confidence_measure", "top") == "gap":  # FREE: top-1 minus top-2 probability
+            best = torch.softmax(logits.float(), -1).topk(2, -1).values
+            top = best[:, 0] - best[:, 1]
+        else:
+            top = torch.softmax(logits.float(), -1).gather(1, d[:, None])[:, 0]
         return drafter.to_target(d), None, top
 
     def _draft_chain(self, st: _State) -> tuple[torch.Tensor, torch.Tensor, torch.Tensor | None]:
@@ -437,8 +445,11 @@ class SpecEngine:
         if self.min_confidence is not None:
             # stop after the first draft whose confidence is below the threshold (the first draft always stays)
             low = torch.stack(confs, 1) < self.min_confidence
-            stop = torch.cumsum(low.int(), 1) - low.int() > 0  # a low-confidence draft before this one
-            stop[:, 0] = False
+            if getattr(drafter, "stop_inclusive", False):  # the low-confidence token itself goes to the exact pass
+                stop = torch.cumsum(low.int(), 1) > 0
+            else:
+                stop = torch.cumsum(low.int(), 1) - low.int() > 0  # a low-confidence draft before this one
+                stop[:, 0] = False
             drafts = torch.where(stop, torch.full_like(drafts, -1), drafts)
         parents = (torch.arange(k, device=dev) - 1).expand(batch, k).contiguous()  # -1: child of the root
         q_full = torch.stack(qs, 1) if self.rejection else None

@@ -83,6 +83,7 @@ class CausalLM(nn.Module):
         self.kv_evictor = None
         #: KV coder (kivi): codes committed chunks after every commit; attention reads the codes
         self.kv_quantizer = None
+        self.depth_policy = None  # dynamic depth (per-token layer skipping / early exit) of the exact passes
         self.kv_scales: tuple[torch.Tensor, torch.Tensor] | None = None
         #: tensor-parallel group (set by economize_b200.parallel.tp.shard_model) and this rank's shard sizes
         self.tp = None
@@ -143,13 +144,19 @@ class CausalLM(nn.Module):
         aux: dict[int, torch.Tensor] = {}
         todo = layers if layers is not None else range(c.num_layers)
         partial = False  # h is a row-parallel partial awaiting its all-reduce (tensor parallelism)
+        depth = self.depth_policy if self.depth_policy is not None and self.depth_policy.acts(batch) else None
+        if depth is not None:
+            depth.begin_pass(batch, h)
         for i in todo:
             layer = self.layers[i]
+            gated = depth is not None and depth.gates(i)
+            x_in = None
             # a layer view may skip a sublayer (self-drafting): the pending branch output is added at the next norm
             if not getattr(layer, "skip_attn", False):
                 x, resid = self._norm(h, layer.attn_norm, resid, partial)
                 if i in capture:
                     aux[i] = resid
+                x_in = resid
                 h = self._attention(layer, i, x, batch, cache, cos, sin)
                 partial = True
             elif i in capture:
@@ -158,6 +165,10 @@ class CausalLM(nn.Module):
                 x, resid = self._norm(h, layer.mlp_norm, resid, partial)
                 h = self._mlp(layer, x, i)
                 partial = True
+            if gated and x_in is not None:
+                # dynamic depth: the policy decides, per token, how the layer's output enters the stream
+                out = resid + self._materialize(h, partial)
+                h, resid, partial = depth.combine(i, x_in, out, batch), None, False
         out, resid = self._norm(h, self.norm, resid, partial)
         if c.num_layers in capture:
             aux[c.num_layers] = resid
@@ -166,6 +177,19 @@ class CausalLM(nn.Module):
         if -2 in capture:
             aux[-2] = resid
         return out, aux
+
+    def _materialize(self, h, partial: bool) -> torch.Tensor:
+        """A branch output as a plain tensor: split-K partials summed, a row-parallel partial all-reduced."""
+        if isinstance(h, ops.Partials):
+            h = h.sum()
+        tp = self.tp
+        if partial and tp is not None and tp.size > 1:
+            from ..parallel.comm import Pushed
+
+            if isinstance(h, Pushed):
+                raise ValueError("dynamic depth needs the all-reduced branch output; disable the fused push mode")
+            h = tp.all_reduce(h)
+        return h
 
     def _norm(self, h: torch.Tensor, weight: torch.Tensor, resid: torch.Tensor | None,
               partial: bool) -> tuple[torch.Tensor, torch.Tensor]:
