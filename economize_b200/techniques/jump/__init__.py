@@ -1,0 +1,179 @@
+"""Cross-layer jump drafting (``jump``; economize ``techniques/jump``). Between two exact passes each draft token
+skips the target's layers ``1 .. m`` (and ``r + 1 .. L``): a predictor maps the previous token's state after layer
+``u`` and the new token's embedding to the new token's state after layer ``m``, and only the target's layers
+``m + 1 .. r`` run, against the target's own cache (the committed K/V of those layers are exact; the drafts write
+theirs into the scratch slots past the committed length, which the verification pass overwrites). The exit reads
+through the final norm and LM head. The target verifies (lossless).
+
+The objective ``jump_rollout`` fits the predictor by teacher forcing: from the target's own states after layer
+``u`` at ``t`` and the embedding of token ``t + 1`` to the state after layer ``m`` at ``t + 1`` (normalised squared
+error); economize's open-loop rollouts, source mixers and RL pieces are not built.
+"""
+
+from __future__ import annotations
+
+from dataclasses import dataclass
+from typing import ClassVar
+
+import torch
+import torch.nn.functional as F
+from torch import nn
+
+from ...core.technique import Capability, Family, Technique, TechniqueConfig, register_technique
+from ...decoding.config import DecodeConfig
+from ...errors import ConfigError
+from ...runtime.cache import StepBatch
+from ...train.objective import OBJECTIVES, Objective, OptimDefaults
+from ...validation import check_choice, check_positive
+
+__all__ = ["JumpConfig", "JumpDrafter", "JumpPredictor", "JumpTechnique"]
+
+
+@dataclass(frozen=True)
+class JumpConfig(TechniqueConfig):
+    """``target_layer`` ``m`` and ``source_layer`` ``u`` (1-indexed, ``m <= u``); ``exit_layer`` ``r`` (``None``:
+    the last layer); ``predictor``: ``"mlp"``; ``width``: the predictor's inner width multiple of the hidden size."""
+
+    technique: ClassVar[str] = "jump"
+    target_layer: int | None = None
+    source_layer: int | None = None
+    exit_layer: int | None = None
+    predictor: str = "mlp"
+    width: float = 1.0
+    param_dtype: str = "float32"
+
+    def __post_init__(self) -> None:
+        check_choice("predictor", self.predictor, ("mlp",))
+        check_positive("width", self.width)
+        check_choice("param_dtype", self.param_dtype, ("float32", "model"))
+
+    def resolved(self, num_layers: int) -> tuple[int, int, int]:
+        m = self.target_layer or max(1, num_layers // 3)
+        u = self.source_layer or max(m, (num_layers * 9) // 16)
+        r = self.exit_layer or num_layers
+        return m, u, r
+
+    def validate(self, model) -> None:
+        n = model.config.num_layers
+        m, u, r = self.resolved(n)
+        if not 1 <= m <= u <= r <= n or m >= r:
+            raise ConfigError(f"jump needs 1 <= target_layer <= source_layer <= exit_layer <= {n} and "
+                              f"target_layer < exit_layer, got {(m, u, r)}")
+
+
+class JumpPredictor(nn.Module):
+    """``e + W2 silu(W1 [s_u; e])``: starts as the embedding itself."""
+
+    def __init__(self, hidden: int, width: int) -> None:
+        super().__init__()
+        self.w1 = nn.Linear(2 * hidden, width)
+        self.w2 = nn.Linear(width, hidden)
+        nn.init.zeros_(self.w2.weight)
+        nn.init.zeros_(self.w2.bias)
+
+    def forward(self, source: torch.Tensor, emb: torch.Tensor) -> torch.Tensor:
+        dt = self.w1.weight.dtype
+        e = emb.to(dt)
+        return e + self.w2(F.silu(self.w1(torch.cat([source.to(dt), e], -1))))
+
+
+class JumpDrafter:
+    def __init__(self, tech: JumpTechnique) -> None:
+        self.tech = tech
+        self.m, self.u, self.r = tech.layers
+        self.capture_layers = (self.u,)
+        self.carry_size = tech.model.config.hidden_size
+        self.cache = None
+
+    def begin(self, batch: int, capacity: int) -> None:
+        pass
+
+    def bind_target_cache(self, cache) -> None:
+        self.cache = cache
+
+    def fuse(self, aux):
+        return aux[self.u]
+
+    def _run(self, tokens, states, batch: StepBatch):
+        tech = self.tech
+        model = tech.model
+        h_m = tech.predictor(states, model.embed_tokens(tokens.clamp_min(0))).to(model.dtype)
+        cap = (-2,) if self.u == self.r else (self.u,)
+        out, aux = model.forward_step(tokens.clamp_min(0), batch, self.cache, capture=cap,
+                                      layers=range(self.m, self.r), hidden=h_m)
+        nxt = aux[cap[0]]
+        return model.logits(out).float(), nxt
+
+    def observe(self, tokens, sources, kv_len, n_valid, root):
+        b = tokens.shape[0]
+        rows = torch.arange(b, device=tokens.device)
+        r = root.long()
+        slot = (kv_len + root).to(torch.int32)
+        one = torch.ones(b, dtype=torch.int32, device=tokens.device)
+        logits, nxt = self._run(tokens[rows, r][:, None], sources[rows, r][:, None],
+                                StepBatch(slot, one, slot[:, None].contiguous()))
+        return logits[:, 0], nxt[:, 0]
+
+    def tree_step(self, tokens, states, positions, kv_base, n_forwarded, q_offset, mask):
+        batch = tokens.shape[0]
+        n_new = torch.full((batch,), n_forwarded, dtype=torch.int32, device=tokens.device)
+        return self._run(tokens, states, StepBatch(kv_base.to(torch.int32), n_new, positions.to(torch.int32), mask,
+                                                   q_offset))
+
+    def to_target(self, ids):
+        return ids
+
+
+@register_technique
+class JumpTechnique(Technique):
+    config_class = JumpConfig
+    capabilities = Capability.DRAFTER
+    family = Family.DRAFTER
+    lossless = True
+    objective_name = "jump_rollout"
+
+    def __init__(self, config: JumpConfig, model) -> None:
+        super().__init__(config, model)
+        h = model.config.hidden_size
+        self.layers = config.resolved(model.config.num_layers)
+        dtype = torch.float32 if config.param_dtype == "float32" else model.dtype
+        self.predictor = JumpPredictor(h, max(8, int(config.width * h))).to(device=model.device, dtype=dtype)
+
+    def drafter(self):
+        return JumpDrafter(self)
+
+    def default_decoding(self) -> DecodeConfig:
+        return DecodeConfig(cycle_length=5)
+
+
+@OBJECTIVES.register("jump_rollout")
+class JumpRollout(Objective):
+    """Normalised squared error between the predicted and the target's state after layer ``m`` at ``t + 1``."""
+
+    name = "jump_rollout"
+    defaults = OptimDefaults(lr=1e-3, warmup_steps=0)
+
+    def __init__(self, model) -> None:
+        super().__init__(model)
+        if "jump" not in model.techniques:
+            raise ConfigError("jump_rollout needs an attached jump technique")
+        self.tech = model.techniques["jump"]
+
+    def parameters(self):
+        return list(self.tech.predictor.parameters())
+
+    def loss(self, tokens: torch.Tensor):
+        tech = self.tech
+        model = tech.model
+        m, u, _ = tech.layers
+        b, s = tokens.shape
+        with torch.no_grad():
+            cache = model.new_cache(b, ((s + 127) // 128) * 128)
+            lengths = torch.full((b,), s, dtype=torch.int32, device=tokens.device)
+            _, aux = model.forward_step(tokens, StepBatch.prefill(lengths, s), cache, capture=(m, u))
+            emb = model.embed_tokens(tokens)
+        pred = tech.predictor(aux[u][:, :-1].float(), emb[:, 1:].float())
+        target = aux[m][:, 1:].float()
+        err = (pred.float() - target).pow(2).sum(-1) / target.pow(2).sum(-1).clamp_min(1e-6)
+        loss = err.mean()
+        return loss, {"loss": float(loss.detach())}

@@ -1,0 +1,68 @@
+"""Hydra, ReDrafter, PARD and cross-layer jump drafting: lossless under greedy verification (chains and dynamic
+trees), and their objectives train."""
+
+import pytest
+import torch
+
+import economize_b200 as eco
+from economize_b200.techniques.hydra import HydraConfig
+from economize_b200.techniques.jump import JumpConfig
+from economize_b200.techniques.pard import PardConfig
+from economize_b200.techniques.redrafter import RedrafterConfig
+from economize_b200.train.objective import OBJECTIVES
+
+from .helpers import prompts, tiny_model
+
+CAL = torch.randint(0, 1024, (2, 32), generator=torch.Generator().manual_seed(3))
+TREE = eco.DecodeConfig(cycle_length=5, draft_policy="dynamic_tree",
+                        draft_policy_options={"depth": 4, "topk": 4, "total_tokens": 16})
+
+
+@pytest.fixture(scope="module")
+def model():
+    return tiny_model()
+
+
+@pytest.fixture(scope="module")
+def plain(model):
+    return eco.apply(model).decode_batch(prompts(), 20, decoding=eco.DecodeConfig(cycle_length=1))
+
+
+@pytest.mark.parametrize("make,decoding", [
+    (lambda: HydraConfig(num_heads=4), None),
+    (lambda: HydraConfig(num_heads=4), TREE),
+    (lambda: RedrafterConfig(beam_width=4, beam_length=4), None),
+    (lambda: RedrafterConfig(beam_length=4), eco.DecodeConfig(cycle_length=4)),
+    (lambda: PardConfig(model=tiny_model(num_layers=2, seed=1), max_drafts=4), None),
+    (lambda: JumpConfig(target_layer=1, source_layer=2), None),
+    (lambda: JumpConfig(target_layer=1, source_layer=3, exit_layer=3), TREE),
+])
+def test_lossless(model, plain, make, decoding):
+    em = eco.apply(model, make())
+    out = em.decode_batch(prompts(), 20, decoding=decoding)
+    for a, b in zip(plain, out):
+        assert torch.equal(a.tokens, b.tokens)
+
+
+def test_pard_self_draft_accepts(model, plain):
+    # the target itself as the PARD model: the first draft of every cycle is the target's own next token
+    em = eco.apply(model, PardConfig(model=model, max_drafts=3))
+    out = em.decode_batch(prompts(), 20)
+    assert sum(r.accepted for r in out) > 0
+
+
+@pytest.mark.parametrize("cfg,name", [(HydraConfig(num_heads=3), "step_distill"),
+                                      (RedrafterConfig(beam_length=3), "step_distill"),
+                                      (JumpConfig(target_layer=1, source_layer=2), "jump_rollout")])
+def test_objectives_train(cfg, name):
+    em = eco.apply(tiny_model(), cfg)
+    obj = OBJECTIVES.get(name)(em)
+    opt = torch.optim.Adam(obj.parameters(), lr=2e-3)
+    losses = []
+    for _ in range(8):
+        loss, _ = obj.loss(CAL)
+        opt.zero_grad()
+        loss.backward()
+        opt.step()
+        losses.append(float(loss.detach()))
+    assert min(losses[1:]) < losses[0], losses
