@@ -5,6 +5,7 @@ import pytest
 import torch
 
 import economize_b200 as eco
+from economize_b200.techniques.dflash import DFlashConfig
 from economize_b200.techniques.hydra import HydraConfig
 from economize_b200.techniques.jump import JumpConfig
 from economize_b200.techniques.pard import PardConfig
@@ -36,6 +37,8 @@ def plain(model):
     (lambda: PardConfig(model=tiny_model(num_layers=2, seed=1), max_drafts=4), None),
     (lambda: JumpConfig(target_layer=1, source_layer=2), None),
     (lambda: JumpConfig(target_layer=1, source_layer=3, exit_layer=3), TREE),
+    (lambda: DFlashConfig(block_size=5), None),
+    (lambda: DFlashConfig(block_size=5), TREE),
 ])
 def test_lossless(model, plain, make, decoding):
     em = eco.apply(model, make())
