@@ -183,3 +183,54 @@ def test_ep2_fused_dispatch_combine():
                 p.kill()
     for rank, res in results.items():
         assert "error" not in res and all(res.values()), (rank, res)
+
+
+def _ssd_worker(rank, world, port, queue):
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), RANK=str(rank), WORLD_SIZE=str(world),
+                      LOCAL_RANK=str(rank), NCCL_NVLS_ENABLE="0")
+    import datetime
+
+    import torch.distributed as dist
+
+    import economize_b200 as eco
+    from economize_b200.parallel.ssd import AsyncSpeculativeDecoder, SSDConfig
+
+    from .helpers import gpu_tiny_model, prompts
+
+    torch.cuda.set_device(rank)
+    dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=60))
+    dev = torch.device("cuda", rank)
+    result = {}
+    try:
+        model = gpu_tiny_model(dev)  # the same weights on both ranks: every speculation hits
+        prompt = prompts((40,))[0].to(dev)
+        res = AsyncSpeculativeDecoder(model, SSDConfig(draft_length=4, fanout=2)).generate(prompt, 24)
+        if rank == 0:
+            plain = eco.apply(model).decode(prompt, 24, decoding=eco.DecodeConfig(cycle_length=1)).tokens
+            result["tokens"] = bool(torch.equal(res.tokens.cpu(), plain.cpu()))
+            result["hits"] = res.hits == res.rounds - 1
+    except Exception as err:  # report instead of hanging the other rank
+        result["error"] = f"{type(err).__name__}: {err}"
+    torch.cuda.synchronize()
+    queue.put((rank, result))
+    dist.destroy_process_group()
+
+
+def test_ssd_two_gpus():
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs 2 GPUs")
+    ctx = mp.get_context("spawn")
+    queue = ctx.Queue()
+    port = _port()
+    procs = [ctx.Process(target=_ssd_worker, args=(r, 2, port, queue), daemon=True) for r in range(2)]
+    for p in procs:
+        p.start()
+    try:
+        results = dict(queue.get(timeout=240) for _ in procs)
+    finally:
+        for p in procs:
+            p.join(timeout=30)
+            if p.is_alive():
+                p.kill()
+    for rank, res in results.items():
+        assert "error" not in res and all(res.values()), (rank, res)
