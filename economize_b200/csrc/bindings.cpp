@@ -853,6 +853,23 @@ Tensor glu_rows(Tensor x, Tensor w_gate_up, c10::optional<Tensor> gate, c10::opt
   return h.view(sizes);
 }
 
+// ---- binary factors (binary.cu) ---------------------------------------------------------------------------------
+// x [M <= 16, K] fp32 times the sign matrix bits [N, ceil(K / 32)] (int32 words, bit set = -1) -> [M, N] fp32.
+Tensor sign_matvec(Tensor bits, Tensor x) {
+  CHECK_CUDA(x);
+  TORCH_CHECK(x.scalar_type() == at::kFloat && bits.scalar_type() == at::kInt, "sign_matvec: fp32 x, int32 bits");
+  c10::cuda::CUDAGuard guard(x.device());
+  x = x.contiguous();
+  bits = bits.contiguous();
+  const int M = static_cast<int>(x.size(0)), K = static_cast<int>(x.size(1)), N = static_cast<int>(bits.size(0));
+  TORCH_CHECK(bits.size(1) == (K + 31) / 32, "sign_matvec: bits [N, ceil(K / 32)]");
+  auto out = at::empty({M, N}, x.options());
+  const int rc = ecz::launch_sign_matvec(reinterpret_cast<const uint32_t*>(bits.data_ptr<int>()), x.data_ptr<float>(),
+                                         out.data_ptr<float>(), M, N, K, at::cuda::getCurrentCUDAStream());
+  TORCH_CHECK(rc == 0, "sign_matvec: at most 16 rows");
+  return out;
+}
+
 // ---- expert parallelism over NVLink peer memory (ep.cu) ---------------------------------------------------------
 int64_t ep_buffer_bytes(int64_t world, int64_t experts_local, int64_t cap, int64_t hidden, int64_t ret_rows) {
   return ecz::ep_layout(static_cast<int>(world), static_cast<int>(experts_local), static_cast<int>(cap),
@@ -1040,6 +1057,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("sample", &sample, "inverse-CDF draw of one token per probability row");
   m.def("rejection", &rejection, "lossless speculative sampling of a draft chain (accept/reject + resample)");
   m.def("ngram", &ngram, "prompt-lookup draft proposals from the token history");
+  m.def("sign_matvec", &sign_matvec, "x times a packed sign matrix (LittleBit factors, <= 16 rows)");
   m.def("colsparse_linear", &colsparse_linear, "activation-sparse GEMV over a transposed weight (<= 16 rows)");
   m.def("glu_rows", &glu_rows, "gated-MLP hidden over the kept channels only (CATS / Deja Vu, <= 16 rows)");
   m.def("ep_buffer_bytes", &ep_buffer_bytes, "bytes of one rank's expert-parallel symmetric buffer");

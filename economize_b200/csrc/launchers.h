@@ -152,6 +152,9 @@ int launch_colsparse_gemv(const void* x, int ldx, const void* wt, const float* t
 int launch_glu_rows(const void* x, int ldx, const void* w, const void* gate_pre, int ld_gate, const uint8_t* keep,
                     const float* thr, void* h, int M, int F, int H, cudaStream_t stream);
 
+// binary.cu: out[m, n] = sum_k s[n, k] x[m, k] with sign bits packed 32 per word along k (bit set = -1), M <= 16.
+int launch_sign_matvec(const uint32_t* bits, const float* x, float* out, int M, int N, int K, cudaStream_t stream);
+
 // ep.cu: expert-parallel dispatch / combine over IPC-mapped symmetric buffers (layout below, per rank).
 struct EpLayout {
   int world = 1, experts_local = 1, cap = 1, hidden = 8, ret_rows = 1;
