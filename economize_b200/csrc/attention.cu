@@ -239,6 +239,17 @@ __global__ void __launch_bounds__(kThreads, 1)
       tma_load_2d(v_tiles + s * kTile + kAtom, &tm_v, &kv_full[s], 64, y);
     }
   };
+  // Chunks whose committed keys are all hidden by the keep bitmap (and that hold no new key) are skipped: the
+  // CTA walks the active chunks only, every thread computing the same sequence from the bitmap.
+  auto active = [&](int c) -> bool {
+    if (keep == nullptr || (c + 1) * kKeys > base) return true;
+    const uint32_t* kw = keep + (static_cast<size_t>(b) * Hkv + kvh) * (S / 32) + c * (kKeys / 32);
+    return (kw[0] | kw[1] | kw[2] | kw[3]) != 0u;
+  };
+  auto next_active = [&](int c) -> int {
+    while (c < c1 && !active(c)) ++c;
+    return c;
+  };
   if constexpr (FP8) scale_log2 *= k_scale[kvh];  // S = s_k * (Q . K8^T)
   if (tid == 0) {
     mbar_init(&kv_full[0], 1);
@@ -247,9 +258,11 @@ __global__ void __launch_bounds__(kThreads, 1)
     mbar_init(bar_pv, 1);
     *abort_flag = 0;
     fence_mbar_init();
-    // the first two K/V chunks stream while the CTA allocates TMEM and stages Q
-    if (c0 < c1) issue_kv(c0, 0);
-    if (c0 + 1 < c1) issue_kv(c0 + 1, 1);
+    // the first two active K/V chunks stream while the CTA allocates TMEM and stages Q
+    const int a0 = next_active(c0);
+    const int a1 = a0 < c1 ? next_active(a0 + 1) : c1;
+    if (a0 < c1) issue_kv(a0, 0);
+    if (a1 < c1) issue_kv(a1, 1);
   }
   __syncwarp();
   if (warp == 0) tmem_alloc(tmem_slot, 256);
@@ -282,8 +295,10 @@ __global__ void __launch_bounds__(kThreads, 1)
   constexpr uint32_t idesc_pv = idesc_bf16_f32(kRows, kDim, /*b_mn_major=*/true);
   bool ok = true;
 
-  for (int c = c0; c < c1 && ok; ++c) {
-    const int i = c - c0;
+  int c = next_active(c0);
+  int c_next = c < c1 ? next_active(c + 1) : c1;
+  for (int i = 0; c < c1 && ok; ++i) {
+    const int c_after = c_next < c1 ? next_active(c_next + 1) : c1;  // the chunk two ahead (prefetched below)
     const int s = i & 1;
     const uint32_t kv_phase = (i >> 1) & 1;
     const uint32_t ph = i & 1;
@@ -371,7 +386,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     tc_fence_before();
     __syncthreads();
     if constexpr (FP8) {  // every thread has converted stage s: its raw codes may be overwritten
-      if (tid == 0 && c + 2 < c1) issue_kv(c + 2, s);
+      if (tid == 0 && c_after < c1) issue_kv(c_after, s);
     }
     if (tid == 0) {
       tc_fence_after();
@@ -390,13 +405,15 @@ __global__ void __launch_bounds__(kThreads, 1)
     __syncwarp();
     tc_fence_after();
     if (stamp && i == 0) stamp[5] = global_timer_ns();
-    if (!FP8 && tid == 0 && c + 2 < c1) issue_kv(c + 2, s);  // both MMAs reading stage s are done
+    if (!FP8 && tid == 0 && c_after < c1) issue_kv(c_after, s);  // both MMAs reading stage s are done
     __syncwarp();
     float pv[32];
     tmem_ld16(tmem_pv + lane_off, pv);
     tmem_ld16(tmem_pv + lane_off + 16, pv + 16);
 #pragma unroll
     for (int d = 0; d < 32; ++d) o[d] = o[d] * alpha + pv[d];
+    c = c_next;
+    c_next = c_after;
   }
   if (stamp) stamp[6] = global_timer_ns();
   tc_fence_before();

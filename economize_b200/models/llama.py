@@ -84,6 +84,7 @@ class CausalLM(nn.Module):
         #: KV coder (kivi): codes committed chunks after every commit; attention reads the codes
         self.kv_quantizer = None
         self.depth_policy = None  # dynamic depth (per-token layer skipping / early exit) of the exact passes
+        self.prefill_sparsity = None  # sparse prefill attention (MInference), run as a chunked prefill
         self.kv_scales: tuple[torch.Tensor, torch.Tensor] | None = None
         #: tensor-parallel group (set by economize_b200.parallel.tp.shard_model) and this rank's shard sizes
         self.tp = None
@@ -138,6 +139,10 @@ class CausalLM(nn.Module):
         final-normed states again, ``-2``: the residual stream after the last block that ran). ``hidden`` replaces
         the embeddings as the input of the first block that runs (with ``layers``: one block on given inputs)."""
         c = self.config
+        sparse = self.prefill_sparsity
+        if sparse is not None and not sparse.active and hidden is None and layers is None and \
+                sparse.covers(tokens, batch):
+            return sparse.chunked_forward(self, tokens, batch, cache, capture)
         cos, sin = self.rope_tables()
         h = self.embed_tokens(tokens) if hidden is None else hidden
         resid: torch.Tensor | None = None
@@ -221,6 +226,11 @@ class CausalLM(nn.Module):
                            v_cache, batch.kv_len, batch.n_new, layer.q_norm, layer.k_norm, c.rms_norm_eps,
                            q_offset=batch.q_offset, k_scale=k_scale, v_scale=v_scale)
         keep = self.kv_evictor.keep_for(index, k_cache, q, batch) if self.kv_evictor is not None else None
+        sparse = self.prefill_sparsity
+        if sparse is not None and sparse.active:  # sparse prefill (MInference): keys the chunk's pattern hides
+            pattern = sparse.keep_for(index, k_cache, q, batch)
+            if pattern is not None:
+                keep = pattern if keep is None else keep & pattern
         kivi = self.kv_quantizer.layer_args(index, cache) if self.kv_quantizer is not None else {}
         o = ops.attention(q, k_cache, v_cache, batch.kv_len, batch.n_new, batch.mask, q_offset=batch.q_offset,
                           k_scale=k_scale, v_scale=v_scale, keep=keep, **kivi)

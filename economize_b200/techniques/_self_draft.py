@@ -72,6 +72,7 @@ def layer_view(target: CausalLM, layers: Sequence[int | tuple[int, bool, bool]],
     view.kv_evictor = None
     view.kv_quantizer = None
     view.depth_policy = None
+    view.prefill_sparsity = None
     if target.kv_scales is not None:
         idx = [spec if isinstance(spec, int) else spec[0] for spec in layers]
         ks, vs = target.kv_scales
