@@ -23,6 +23,9 @@ using at::Tensor;
 
 #define CHECK_CUDA(x) TORCH_CHECK((x).is_cuda(), #x " must be a CUDA tensor")
 #define CHECK_BF16(x) TORCH_CHECK((x).scalar_type() == at::kBFloat16, #x " must be bfloat16")
+// every tensor a kernel dereferences must live on the launching tensor's CUDA device (a host pointer faults)
+#define CHECK_ON(x, ref)                                                                                         \
+  TORCH_CHECK((x).is_cuda() && (x).get_device() == (ref).get_device(), #x " must be on the device of " #ref)
 #define CHECK_I32(x) TORCH_CHECK((x).scalar_type() == at::kInt, #x " must be int32")
 #define CHECK_I64(x) TORCH_CHECK((x).scalar_type() == at::kLong, #x " must be int64")
 
@@ -172,6 +175,13 @@ Tensor rope_store(Tensor qkv, Tensor positions, Tensor cos, Tensor sin, int64_t 
   CHECK_I32(positions);
   CHECK_I32(kv_len);
   CHECK_I32(n_new);
+  CHECK_ON(positions, qkv);
+  CHECK_ON(kv_len, qkv);
+  CHECK_ON(n_new, qkv);
+  CHECK_ON(cos, qkv);
+  CHECK_ON(sin, qkv);
+  CHECK_ON(k_cache, qkv);
+  CHECK_ON(v_cache, qkv);
   TORCH_CHECK(cos.scalar_type() == at::kFloat && sin.scalar_type() == at::kFloat, "rope tables must be fp32");
   TORCH_CHECK(k_cache.dim() == 4, "rope_store expects caches [B, Hkv, S, D]");
   TORCH_CHECK(k_cache.is_contiguous() && v_cache.is_contiguous(), "caches must be contiguous");
@@ -204,6 +214,15 @@ Tensor attention(Tensor q, Tensor k_cache, Tensor v_cache, Tensor kv_len, Tensor
   TORCH_CHECK(v_cache.scalar_type() == k_cache.scalar_type(), "K and V caches must share a dtype");
   CHECK_I32(kv_len);
   CHECK_I32(n_new);
+  CHECK_ON(kv_len, q);
+  CHECK_ON(n_new, q);
+  CHECK_ON(k_cache, q);
+  CHECK_ON(v_cache, q);
+  if (mask.has_value()) CHECK_ON(*mask, q);
+  if (keep.has_value()) CHECK_ON(*keep, q);
+  if (lse_out.has_value()) CHECK_ON(*lse_out, q);
+  if (kivi.has_value()) CHECK_ON(*kivi, q);
+  if (kivi_chunks.has_value()) CHECK_ON(*kivi_chunks, q);
   TORCH_CHECK(q.dim() == 4 && k_cache.dim() == 4, "attention expects q [B, T, H, D] and caches [B, Hkv, S, D]");
   TORCH_CHECK(k_cache.is_contiguous() && v_cache.is_contiguous(), "caches must be contiguous");
   c10::cuda::CUDAGuard guard(q.device());
@@ -552,6 +571,12 @@ void attention_scores(Tensor q, Tensor k_cache, Tensor kv_len, Tensor n_new, c10
   TORCH_CHECK(scores.scalar_type() == at::kFloat && scores.is_contiguous() &&
                   scores.numel() == static_cast<int64_t>(B) * Hkv * S, "scores must be fp32 [B, Hkv, S]");
   TORCH_CHECK(lse2.scalar_type() == at::kFloat && lse2.numel() == static_cast<int64_t>(B) * T * H, "lse2 [B, T, H]");
+  CHECK_ON(k_cache, q);
+  CHECK_ON(scores, q);
+  CHECK_ON(lse2, q);
+  CHECK_ON(kv_len, q);
+  CHECK_ON(n_new, q);
+  if (mask.has_value()) CHECK_ON(*mask, q);
   Tensor m;
   if (mask.has_value()) {
     m = mask->contiguous();
@@ -572,6 +597,10 @@ void kivi_quantize(Tensor cache, Tensor kivi, Tensor kv_len, Tensor chunks, int6
   CHECK_BF16(cache);
   CHECK_I32(kv_len);
   CHECK_I32(chunks);
+  CHECK_CUDA(cache);
+  CHECK_ON(kivi, cache);
+  CHECK_ON(kv_len, cache);
+  CHECK_ON(chunks, cache);
   TORCH_CHECK(cache.dim() == 6 && cache.is_contiguous(), "cache must be a contiguous [L, 2, B, Hkv, S, D] tensor");
   c10::cuda::CUDAGuard guard(cache.device());
   const int L = static_cast<int>(cache.size(0)), B = static_cast<int>(cache.size(2)), Hkv = static_cast<int>(cache.size(3));
@@ -656,6 +685,9 @@ std::tuple<Tensor, Tensor, Tensor> greedy_accept(Tensor tokens, Tensor parents, 
   CHECK_I64(tokens);
   CHECK_I64(parents);
   CHECK_I64(pred);
+  CHECK_ON(parents, tokens);
+  CHECK_ON(pred, tokens);
+  if (ok.has_value()) CHECK_ON(*ok, tokens);
   c10::cuda::CUDAGuard guard(tokens.device());
   tokens = tokens.contiguous();
   parents = parents.contiguous();
@@ -683,6 +715,9 @@ void kv_compact(Tensor cache, Tensor kv_len, Tensor path, Tensor n_acc) {
   CHECK_I32(kv_len);
   CHECK_I32(path);
   CHECK_I32(n_acc);
+  CHECK_ON(kv_len, cache);
+  CHECK_ON(path, cache);
+  CHECK_ON(n_acc, cache);
   TORCH_CHECK(cache.dim() == 6 && cache.is_contiguous(), "cache must be a contiguous [L, 2, B, Hkv, S, D] tensor");
   c10::cuda::CUDAGuard guard(cache.device());
   path = path.contiguous();
@@ -716,6 +751,8 @@ std::tuple<Tensor, Tensor> rejection(Tensor p, Tensor q, Tensor drafts, Tensor u
   CHECK_CUDA(p);
   TORCH_CHECK(p.scalar_type() == at::kFloat && q.scalar_type() == at::kFloat, "p and q must be fp32");
   CHECK_I64(drafts);
+  CHECK_ON(q, p);
+  CHECK_ON(drafts, p);
   c10::cuda::CUDAGuard guard(p.device());
   p = p.contiguous();
   q = q.contiguous();
@@ -888,6 +925,11 @@ Tensor ep_moe(Tensor xs, Tensor offsets, Tensor pos, Tensor w, Tensor w_gate_up,
   CHECK_I32(offsets);
   CHECK_I32(pos);
   TORCH_CHECK(w.scalar_type() == at::kFloat, "ep_moe: fp32 routing weights");
+  CHECK_ON(offsets, xs);
+  CHECK_ON(pos, xs);
+  CHECK_ON(w, xs);
+  CHECK_ON(w_gate_up, xs);
+  CHECK_ON(w_down, xs);
   c10::cuda::CUDAGuard guard(xs.device());
   xs = xs.contiguous();
   const int world = static_cast<int>(ptrs.size());

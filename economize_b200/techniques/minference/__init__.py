@@ -83,7 +83,7 @@ class MInferencePrefill:
 
     def chunked_forward(self, model, tokens, batch: StepBatch, cache, capture):
         b, width = tokens.shape
-        lengths = batch.n_new.long()
+        lengths = batch.n_new.long().to(tokens.device)
         outs, auxes = [], []
         self.active = True
         try:

@@ -14,7 +14,8 @@ from .helpers import tiny_model
 def _hidden(model, tokens):
     b, s = tokens.shape
     cache = model.new_cache(b, ((s + 127) // 128) * 128)
-    h, _ = model.forward_step(tokens, StepBatch.prefill(torch.full((b,), s, dtype=torch.int32), s), cache)
+    lengths = torch.full((b,), s, dtype=torch.int32, device=tokens.device)
+    h, _ = model.forward_step(tokens, StepBatch.prefill(lengths, s), cache)
     return h.float()
 
 

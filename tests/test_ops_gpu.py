@@ -281,3 +281,28 @@ def test_topk_logp_matches_torch(cuda, rows, V, k):
     ref = torch.log_softmax(logits, -1).topk(k, -1)
     _close(vals, ref.values, 1e-4, 1e-5)
     assert torch.equal(ids, ref.indices + d2t[ref.indices])
+
+
+@pytest.mark.gpu
+def test_host_index_tensors_are_refused_before_launch(cuda):
+    """Index tensors on the host would be dereferenced as device pointers: the bindings refuse them."""
+    from economize_b200 import ops
+
+    q = torch.randn(1, 1, 4, 128, device=cuda).bfloat16()
+    k = torch.zeros(1, 2, 128, 128, device=cuda).bfloat16()
+    with pytest.raises(RuntimeError, match="must be on the device"):
+        ops.attention(q, k, k.clone(), torch.tensor([5], dtype=torch.int32), torch.tensor([1], dtype=torch.int32))
+
+
+@pytest.mark.gpu
+def test_chunked_prefill_matches_whole_prefill(cuda):
+    import economize_b200 as eco
+
+    from .helpers import gpu_tiny_model, prompts
+
+    model = gpu_tiny_model(cuda)
+    p = [x.to(cuda) for x in prompts((300, 517))]
+    whole = eco.apply(model).decode_batch(p, 12, decoding=eco.DecodeConfig(cycle_length=1))
+    chunked = eco.apply(model).decode_batch(p, 12, decoding=eco.DecodeConfig(cycle_length=1, prefill_chunk=128))
+    for a, b in zip(whole, chunked):
+        assert torch.equal(a.tokens.cpu(), b.tokens.cpu())
