@@ -47,15 +47,21 @@ def test_sparse_patterns_approximate_dense(cfg):
 
 @pytest.mark.gpu
 def test_sparse_prefill_on_gpu_matches_reference_attention(cuda):
+    """The kernel's skipping of hidden key chunks gives the masked attention of the CPU reference (same weights)."""
+    from economize_b200.models.llama import CausalLM
+
     from .helpers import gpu_tiny_model
 
     tokens = torch.randint(0, 1024, (1, 1024), generator=torch.Generator().manual_seed(1)).to(cuda)
     m = gpu_tiny_model(cuda)
-    eco.apply(m, MInferenceConfig(pattern="a_shape", sinks=128, local=256, chunk=256))
-    h = _hidden(m, tokens)
-    # the same sparse prefill through the CPU reference kernels
-    cpu = gpu_tiny_model("cpu").float()
-    eco.apply(cpu, MInferenceConfig(pattern="a_shape", sinks=128, local=256, chunk=256))
+    cpu = CausalLM(m.config, torch.float32, "cpu")
+    cpu.load_state_dict({k: v.float().cpu() for k, v in m.state_dict().items()})
+    cfg = MInferenceConfig(pattern="a_shape", sinks=128, local=256, chunk=256)
+    eco.apply(m, cfg)
+    eco.apply(cpu, cfg)
+    h = _hidden(m, tokens).cpu()
     h_ref = _hidden(cpu, tokens.cpu())
-    rel = (h.cpu() - h_ref).norm() / h_ref.norm()
+    rel = (h - h_ref).norm() / h_ref.norm()
     assert rel < 0.05, float(rel)
+    dense = _hidden(gpu_tiny_model(cuda), tokens).cpu()
+    assert (h - dense).norm() / dense.norm() > 2 * rel  # the pattern did hide keys
