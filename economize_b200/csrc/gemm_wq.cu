@@ -44,9 +44,9 @@ constexpr int kThreads = 192;
 template <int FMT>
 struct WqFmt {
   // int4: 32 B of codes per row and K-block; int8/fp8: 64 B; 2:4 sparse: the 32 kept bf16 values (64 B)
-  static constexpr int kRawRowBytes = FMT == kWqInt4 ? kBK / 2 : kBK;
+  static constexpr int kRawRowBytes = FMT == kWqInt4 ? kBK / 2 : FMT == kWqInt2 ? kBK / 4 : kBK;
   static constexpr int kRawBytes = kBM * kRawRowBytes;
-  static constexpr bool kZeros = FMT == kWqInt4;
+  static constexpr bool kZeros = FMT == kWqInt4 || FMT == kWqInt2;
   // per-stage side data: one bf16 scale per row, or the 2:4 positions (8 B per row)
   static constexpr int kSideBytes = FMT == kWqSp24 ? kBM * 8 : kBM * 2;
 };
@@ -85,6 +85,16 @@ __device__ __forceinline__ uint4 dequant_chunk(const uint32_t* w, int j, __nv_bf
   if constexpr (FMT == kWqInt4) {
 #pragma unroll
     for (int i = 0; i < 4; ++i) out[i] = bf2_bits(__hmul2(__hsub2(nib_pair(w[j], 4 * i), z2), s2));
+  } else if constexpr (FMT == kWqInt2) {
+    // a word holds 16 codes: bits 2m of the low half = k_2m, of the high half = k_2m+1 (m = 0..7); chunk j is the
+    // low (j even) or high (j odd) eight of them
+    const uint32_t word = w[j >> 1];
+    const int base = (j & 1) * 8;
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const __nv_bfloat162 q = bits_bf2(((word >> (base + 2 * i)) & 0x00030003u) | 0x43004300u);  // 128 + code
+      out[i] = bf2_bits(__hmul2(__hsub2(q, z2), s2));
+    }
   } else if constexpr (FMT == kWqInt8) {
     const __nv_bfloat162 c136 = bits_bf2(0x43084308u);  // 136 = 128 + 8
     const __nv_bfloat162 c128 = bits_bf2(0x43004300u);
@@ -397,7 +407,7 @@ int gemm_wq_splits(int M, int N, int K, int fmt, int num_sms) {
   const int tiles = ((N + kBM - 1) / kBM) * ((M + gemm_block_n(M) - 1) / gemm_block_n(M));
   const int kb = K / kBK;
   // at least 8 K-blocks (512 K) per CTA for int8/fp8, 16 for int4: below that the prologue dominates
-  const int min_kb = fmt == kWqInt4 ? 16 : 8;
+  const int min_kb = fmt == kWqInt2 ? 32 : fmt == kWqInt4 ? 16 : 8;
   int splits = std::max(1, std::min(slots / std::max(1, tiles), kb / min_kb));
   return std::min(8, splits);
 }
@@ -411,6 +421,7 @@ int launch_gemm_wq(const WqMaps& maps, void* y, int M, int N, int K, int group, 
     case kWqInt8: return run_wq_bn<kWqInt8>(maps, y, M, N, K, group, splits, status, stream);
     case kWqFp8: return run_wq_bn<kWqFp8>(maps, y, M, N, K, group, splits, status, stream);
     case kWqSp24: return run_wq_bn<kWqSp24>(maps, y, M, N, K, K, splits, status, stream);
+    case kWqInt2: return run_wq_bn<kWqInt2>(maps, y, M, N, K, group, splits, status, stream);
     default: return -1;
   }
 }

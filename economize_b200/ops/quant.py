@@ -13,6 +13,9 @@ Formats (economize's ``QUANT_FORMATS`` names, ``src/economize/techniques/quant/g
 * ``int8``: symmetric codes -128..127, ``w = q * s``; stored as ``q + 128`` with the byte order ``k0 k2 k1 k3`` per
   word (the kernel splits each byte into nibbles to build exact bf16 values).
 * ``fp8``: e4m3 codes, ``w = q * s``.
+* ``int3``: codes 0..7 with zero points, stored in the ``int4`` layout (the kernel's int4 path dequantizes them).
+* ``int2``: codes 0..3 with zero points, 16 per 32-bit word (bits ``2m`` of the low half hold ``k_2m``, of the high
+  half ``k_2m+1``), so the kernel extracts a bf16 pair with one shift and one mask as for int4.
 
 Scales (and zeros) are ``[K / group, N]`` bf16: one 256-byte row per 128 output features and group, which the kernel
 reads with one TMA box. The dequantized weight is ``bf16((q - z) * s)`` in every path (the kernel's bf16x2
@@ -26,10 +29,12 @@ from torch import nn
 
 from ..errors import ConfigError
 
-__all__ = ["FORMAT_CODES", "QWeight", "dequantize", "install", "pack", "unpack"]
+__all__ = ["FORMAT_CODES", "ZERO_POINT_FORMATS", "QWeight", "dequantize", "install", "pack", "unpack"]
 
-#: kernel format codes (``WqFormat`` in ``csrc/launchers.h``)
-FORMAT_CODES = {"int4": 0, "int8": 1, "fp8": 2}
+#: kernel format codes (``WqFormat`` in ``csrc/launchers.h``); int3 codes (0..7) are stored in the int4 layout
+FORMAT_CODES = {"int4": 0, "int8": 1, "fp8": 2, "int3": 0, "int2": 4}
+#: formats with a zero point per (row, group) (the bf16 value ``128 + z``)
+ZERO_POINT_FORMATS = ("int2", "int3", "int4")
 _INT4_ORDER = (0, 2, 4, 6, 1, 3, 5, 7)
 _INT8_ORDER = (0, 2, 1, 3)
 
@@ -48,7 +53,14 @@ def _bytes_to_words(data: torch.Tensor) -> torch.Tensor:
 def pack(codes: torch.Tensor, fmt: str) -> torch.Tensor:
     """Pack integer codes ``[N, K]`` (int4: 0..15, int8: -128..127) or e4m3 values (fp8) into the kernel layout."""
     n, k = codes.shape
-    if fmt == "int4":
+    if fmt == "int2":  # 16 codes per word: bits 2m of the low half = k_2m, of the high half = k_2m+1
+        c = codes.to(torch.int64).reshape(n, k // 16, 8, 2)
+        words = torch.zeros(n, k // 16, dtype=torch.int64, device=codes.device)
+        for m in range(8):
+            words |= (c[..., m, 0] & 3) << (2 * m)
+            words |= (c[..., m, 1] & 3) << (16 + 2 * m)
+        return _words_to_bytes(words)
+    if fmt in ("int4", "int3"):
         c = codes.to(torch.int64).reshape(n, k // 8, 8)[..., list(_INT4_ORDER)]
         words = torch.zeros(n, k // 8, dtype=torch.int64, device=codes.device)
         for i in range(8):
@@ -65,7 +77,14 @@ def pack(codes: torch.Tensor, fmt: str) -> torch.Tensor:
 def unpack(data: torch.Tensor, fmt: str) -> torch.Tensor:
     """Inverse of :func:`pack`: int64 codes (int4, int8) or fp32 values (fp8) ``[N, K]``."""
     n = data.shape[0]
-    if fmt == "int4":
+    if fmt == "int2":
+        words = _bytes_to_words(data)
+        out = torch.empty(n, words.shape[1], 8, 2, dtype=torch.int64, device=data.device)
+        for m in range(8):
+            out[..., m, 0] = (words >> (2 * m)) & 3
+            out[..., m, 1] = (words >> (16 + 2 * m)) & 3
+        return out.reshape(n, -1)
+    if fmt in ("int4", "int3"):
         words = _bytes_to_words(data)
         nib = torch.stack([(words >> (4 * i)) & 0xF for i in range(8)], -1)  # in packed order
         out = torch.empty_like(nib)
@@ -98,7 +117,7 @@ class QWeight(nn.Module):
         qweight: Packed codes (:func:`pack`).
         scales: ``[K / group, N]`` bf16.
         zeros: ``[K / group, N]`` bf16 holding ``128 + z`` (int4), else ``None``.
-        fmt: ``"int4"``, ``"int8"`` or ``"fp8"``.
+        fmt: ``"int2"``, ``"int3"``, ``"int4"``, ``"int8"`` or ``"fp8"``.
         group: Input columns per scale (``in_features`` for one scale per output row).
         dtype: The activation dtype the layer computes in.
     """
@@ -111,7 +130,7 @@ class QWeight(nn.Module):
         self.fmt = fmt
         self.group = int(group)
         self.out_features = int(qweight.shape[0])
-        self.in_features = int(qweight.shape[1] * (2 if fmt == "int4" else 1))
+        self.in_features = int(qweight.shape[1] * {"int4": 2, "int3": 2, "int2": 4}.get(fmt, 1))
         self.compute_dtype = dtype
         self.register_buffer("qweight", qweight.contiguous())
         self.register_buffer("scales", scales.to(torch.bfloat16).contiguous())
@@ -131,7 +150,7 @@ class QWeight(nn.Module):
 
     @property
     def bits(self) -> int:
-        return 4 if self.fmt == "int4" else 8
+        return {"int2": 2, "int3": 3, "int4": 4}.get(self.fmt, 8)
 
     def dequantize(self, dtype: torch.dtype | None = None) -> torch.Tensor:
         return dequantize(self.qweight, self.scales, self.zeros, self.fmt, self.group, dtype or self.compute_dtype)
@@ -161,7 +180,7 @@ class QWeight(nn.Module):
         """The input columns ``[start, stop)`` (a row-parallel shard); both ends must sit on group boundaries."""
         if start % self.group or stop % self.group:
             raise ConfigError(f"column shard [{start}, {stop}) cuts a quantization group of {self.group}")
-        per = 2 if self.fmt == "int4" else 1
+        per = {"int4": 2, "int3": 2, "int2": 4}.get(self.fmt, 1)
         z = None if self.zeros is None else self.zeros[start // self.group: stop // self.group]
         return QWeight(self.qweight[:, start // per: stop // per], self.scales[start // self.group: stop // self.group],
                        z, self.fmt, self.group, self.compute_dtype)

@@ -18,8 +18,8 @@ from ...validation import check_choice, check_positive
 __all__ = ["DraftQuantConfig", "QUANT_FORMATS", "QUANT_METHODS_NAMES", "QuantConfig"]
 
 #: formats the packed kernel layout stores (economize also simulates int2/int3 and fp4 grids)
-QUANT_FORMATS = ("int4", "int8", "fp8", "fp8_block")
-QUANT_METHODS_NAMES = ("rtn", "gptq", "awq")
+QUANT_FORMATS = ("int2", "int3", "int4", "int8", "fp8", "fp8_block")
+QUANT_METHODS_NAMES = ("rtn", "gptq", "awq", "hqq", "smoothquant")
 #: engine projection names and the Hugging Face module names fused into them
 PROJECTIONS = {"wqkv": ("self_attn.q_proj", "self_attn.k_proj", "self_attn.v_proj"), "wo": ("self_attn.o_proj",),
                "w_gate_up": ("mlp.gate_proj", "mlp.up_proj"), "w_down": ("mlp.down_proj",)}
@@ -43,10 +43,13 @@ class QuantConfig(TechniqueConfig):
     """Weight-only quantization of the target's decoder projections.
 
     Args:
-        format: ``"int4"`` (default, GPTQ/AWQ W4A16), ``"int8"`` (W8A16), ``"fp8"`` (e4m3 weights, bf16
+        format: ``"int4"`` (default, GPTQ/AWQ W4A16), ``"int3"`` / ``"int2"`` (W3A16 in the int4 layout, W2A16
+            packed 16 per word), ``"int8"`` (W8A16), ``"fp8"`` (e4m3 weights, bf16
             activations) or ``"fp8_block"`` (W8A8: e4m3 weights with 128 x 128 block scales and activations
             quantised per token and 128-wide block on the fly; ``group_size`` is ignored).
-        method: ``"rtn"`` (round to nearest, no data), ``"gptq"`` (Hessian-aware error feedback, needs
+        method: ``"rtn"`` (round to nearest, no data), ``"hqq"`` (half-quadratic fit of the grid, no data),
+            ``"smoothquant"`` (activation outliers migrated into the weights, then round to nearest: for W8A8 with
+            ``format="fp8_block"``), ``"gptq"`` (Hessian-aware error feedback, needs
             calibration tokens) or ``"awq"`` (activation-aware scaling folded into the preceding norm, then round
             to nearest with clipping search; needs calibration tokens).
         group_size: Input columns per scale (``None``: one scale per output row).
@@ -62,6 +65,8 @@ class QuantConfig(TechniqueConfig):
         awq_grid: AWQ: number of scale exponents and clipping ratios searched.
         awq_clip: AWQ: search per-group clipping thresholds.
         calibration_tokens: Rows of activations kept per projection for AWQ's search.
+        hqq_iters, hqq_p: HQQ: half-quadratic iterations and the ``l_p`` norm of its error model (``p < 1``).
+        smooth_alpha: SmoothQuant's migration strength ``alpha``.
     """
 
     technique: ClassVar[str] = "quant"
@@ -80,6 +85,9 @@ class QuantConfig(TechniqueConfig):
     awq_grid: int = 20
     awq_clip: bool = True
     calibration_tokens: int = 512
+    hqq_iters: int = 20
+    hqq_p: float = 0.7
+    smooth_alpha: float = 0.5
 
     def __post_init__(self) -> None:
         check_choice("method", self.method, QUANT_METHODS_NAMES)
@@ -89,8 +97,11 @@ class QuantConfig(TechniqueConfig):
             raise ConfigError(f"percdamp must lie in [0, 1], got {self.percdamp}")
         if any(int(i) < 1 for i in self.layers):
             raise ConfigError("layers are 1-indexed")
-        if self.method in ("gptq", "awq") and self.format in ("fp8", "fp8_block"):
+        if self.method in ("gptq", "awq", "hqq") and self.format in ("fp8", "fp8_block"):
             raise ConfigError(f"{self.method} fits integer grids; use method='rtn' for fp8")
+        check_positive("hqq_iters", self.hqq_iters)
+        if not 0.0 < self.hqq_p <= 1.0 or not 0.0 <= self.smooth_alpha <= 1.0:
+            raise ConfigError("hqq_p must lie in (0, 1] and smooth_alpha in [0, 1]")
         object.__setattr__(self, "targets", tuple(self.targets))
         object.__setattr__(self, "exclude", tuple(self.exclude))
         object.__setattr__(self, "layers", tuple(int(i) for i in self.layers))
@@ -98,7 +109,7 @@ class QuantConfig(TechniqueConfig):
 
     @property
     def needs_calibration(self) -> bool:
-        return self.method in ("gptq", "awq")
+        return self.method in ("gptq", "awq", "smoothquant")
 
     def validate(self, model) -> None:
         n = model.config.num_layers

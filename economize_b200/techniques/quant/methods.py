@@ -29,6 +29,8 @@ from ...ops.quant import QWeight, pack
 __all__ = ["Grid", "awq_search", "collect", "fit_grid", "gptq", "quantize_codes", "rtn"]
 
 FP8_MAX = 448.0
+#: largest code of the zero-point integer formats
+_INT_TOP = {"int2": 3.0, "int3": 7.0, "int4": 15.0}
 
 
 class Grid:
@@ -44,27 +46,28 @@ class Grid:
 
 def fit_grid(w: torch.Tensor, fmt: str, symmetric: bool, clip: torch.Tensor | float = 1.0) -> Grid:
     """Grid of ``w [N, G, g]`` (groups along the last axis); ``clip`` shrinks the range (AWQ's clipping)."""
-    if fmt == "int4" and not symmetric:
+    top = _INT_TOP.get(fmt)
+    if top is not None and not symmetric:
         hi = (w.amax(-1) * clip).clamp(min=0)
         lo = (w.amin(-1) * clip).clamp(max=0)
         same = (hi - lo) == 0
         lo, hi = torch.where(same, -torch.ones_like(lo), lo), torch.where(same, torch.ones_like(hi), hi)
-        scale = ((hi - lo) / 15.0).to(torch.bfloat16).float()
-        zero = torch.round(-lo / scale).clamp(0, 15)
+        scale = ((hi - lo) / top).to(torch.bfloat16).float()
+        zero = torch.round(-lo / scale).clamp(0, top)
         return Grid(scale, zero)
     amax = w.abs().amax(-1) * clip
-    levels = {"int4": 7.0, "int8": 127.0, "fp8": FP8_MAX}[fmt]
+    levels = {"int2": 1.0, "int3": 3.0, "int4": 7.0, "int8": 127.0, "fp8": FP8_MAX}[fmt]
     scale = (amax / levels).to(torch.bfloat16).float()
     scale = torch.where(scale == 0, torch.ones_like(scale), scale)
-    return Grid(scale, torch.full_like(scale, 8.0) if fmt == "int4" else None)
+    return Grid(scale, torch.full_like(scale, (top + 1) / 2) if top is not None else None)
 
 
 def quantize_codes(w: torch.Tensor, grid: Grid, fmt: str) -> tuple[torch.Tensor, torch.Tensor]:
     """Codes and dequantized values (bf16-rounded, fp32) of ``w [N, G, g]`` on ``grid``."""
     s = grid.scale[..., None]
-    if fmt == "int4":
+    if fmt in _INT_TOP:
         z = grid.zero[..., None]
-        q = torch.clamp(torch.round(w / s) + z, 0, 15)
+        q = torch.clamp(torch.round(w / s) + z, 0, _INT_TOP[fmt])
         return q, ((q - z) * s).to(torch.bfloat16).float()
     if fmt == "int8":
         q = torch.clamp(torch.round(w / s), -128, 127)
@@ -78,7 +81,7 @@ def _qweight(codes: torch.Tensor, grid: Grid, fmt: str, group: int, dtype: torch
     codes = codes.reshape(n, -1)
     packed = pack(codes.to(torch.float8_e4m3fn) if fmt == "fp8" else codes.to(torch.int64), fmt)
     scales = grid.scale.t().contiguous().to(torch.bfloat16)
-    zeros = (grid.zero.t() + 128.0).contiguous().to(torch.bfloat16) if fmt == "int4" else None
+    zeros = (grid.zero.t() + 128.0).contiguous().to(torch.bfloat16) if fmt in _INT_TOP else None
     return QWeight(packed, scales, zeros, fmt, group, dtype)
 
 
@@ -122,7 +125,7 @@ def gptq(weight: torch.Tensor, hessian: torch.Tensor, fmt: str, group: int | Non
     Hinv = torch.linalg.cholesky(torch.cholesky_inverse(L), upper=True)
     codes = torch.zeros_like(W)
     scale = torch.zeros(n, k // g, device=W.device)
-    zero = torch.zeros(n, k // g, device=W.device) if fmt == "int4" else None
+    zero = torch.zeros(n, k // g, device=W.device) if fmt in _INT_TOP else None
     cur: Grid | None = None
     for i1 in range(0, k, blocksize):
         i2 = min(i1 + blocksize, k)
@@ -273,3 +276,55 @@ def awq_clip(weight: torch.Tensor, x: torch.Tensor, fmt: str, group: int, symmet
 
 
 QUANTIZERS: dict[str, Callable] = {"rtn": rtn, "gptq": gptq}
+
+
+# ---- HQQ ------------------------------------------------------------------------------------------------------
+def _shrink_lp(x: torch.Tensor, beta: float, p: float) -> torch.Tensor:
+    """The generalised soft-thresholding of the ``l_p`` proximal step (HQQ, Badri & Shaji 2023)."""
+    return torch.sign(x) * torch.relu(x.abs() - (1.0 / beta) * x.abs().clamp_min(1e-8).pow(p - 1))
+
+
+@torch.no_grad()
+def hqq(weight: torch.Tensor, fmt: str, group: int | None, symmetric: bool, iters: int = 20, p: float = 0.7,
+        beta: float = 10.0, kappa: float = 1.01) -> QWeight:
+    """Half-quadratic quantization: from the min-max grid, alternate ``W_e = shrink_lp(W - W_r)`` (the sparse error
+    the ``l_p`` model tolerates) with the grid that fits ``W - W_e``: the zero point (rounded to the stored integer
+    grid) and, by least squares, the scale. Calibration-free."""
+    g = group or weight.shape[1]
+    w = _groups(weight.float(), g)
+    grid = fit_grid(w, fmt, symmetric)
+    if fmt not in _INT_TOP:
+        codes, _ = quantize_codes(w, grid, fmt)
+        return _qweight(codes, grid, fmt, g, weight.dtype)
+    top = _INT_TOP[fmt]
+    best_err = (quantize_codes(w, grid, fmt)[1] - w).pow(2).sum(-1)
+    best = Grid(grid.scale.clone(), grid.zero.clone())
+    s, z = grid.scale.clone(), grid.zero.clone()
+    for _ in range(iters):
+        q = torch.clamp(torch.round(w / s[..., None]) + z[..., None], 0, top)
+        w_r = (q - z[..., None]) * s[..., None]
+        w_e = _shrink_lp(w - w_r, beta, p)
+        target = w - w_e
+        if not symmetric:
+            z = torch.round((q - target / s[..., None]).mean(-1)).clamp(0, top)
+        c = q - z[..., None]
+        s = ((c * target).sum(-1) / c.pow(2).sum(-1).clamp_min(1e-12)).clamp_min(1e-8).to(torch.bfloat16).float()
+        beta *= kappa
+        cand = Grid(s, z)
+        err = (quantize_codes(w, cand, fmt)[1] - w).pow(2).sum(-1)
+        better = err < best_err
+        best.scale = torch.where(better, s, best.scale)
+        best.zero = torch.where(better, z, best.zero)
+        best_err = torch.minimum(err, best_err)
+    codes, _ = quantize_codes(w, best, fmt)
+    return _qweight(codes, best, fmt, g, weight.dtype)
+
+
+# ---- SmoothQuant ----------------------------------------------------------------------------------------------
+@torch.no_grad()
+def smooth_scales(weights: Sequence[torch.Tensor], stats: _Stats, alpha: float) -> torch.Tensor:
+    """SmoothQuant's per-input-channel scale ``s_j = max|X_j|^alpha / max|W_j|^(1 - alpha)`` (Xiao et al., 2023):
+    the activations are divided by ``s`` (folded into their producer) and the weights multiplied by it."""
+    x_max = stats.sample.abs().amax(0).clamp_min(1e-5)
+    w_max = torch.cat([w.float() for w in weights], 0).abs().amax(0).clamp_min(1e-5)
+    return (x_max.pow(alpha) / w_max.pow(1.0 - alpha)).clamp_min(1e-5)

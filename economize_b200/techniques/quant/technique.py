@@ -70,7 +70,7 @@ class _QuantBase(Technique):
             if "codes" in bufs:
                 self.weights[key] = FP8BlockWeight(bufs["codes"], bufs["scales"], self._dtype())
                 continue
-            k_in = bufs["qweight"].shape[1] * (2 if cfg.format == "int4" else 1)
+            k_in = bufs["qweight"].shape[1] * {"int4": 2, "int3": 2, "int2": 4}.get(cfg.format, 1)
             group = cfg.group_size or k_in
             self.weights[key] = QWeight(bufs["qweight"], bufs["scales"], bufs.get("zeros"), cfg.format, group,
                                         self._dtype())
@@ -140,7 +140,7 @@ class QuantTechnique(_QuantBase):
         if cfg.needs_calibration:
             stats = methods.collect(model, self._batches(), wanted, hessian=cfg.method == "gptq",
                                     keep_rows=cfg.calibration_tokens)
-        if cfg.method == "awq":
+        if cfg.method in ("awq", "smoothquant"):
             self._awq_fold(wanted, stats)
         for i, names in wanted.items():
             layer = model.layers[i]
@@ -157,6 +157,8 @@ class QuantTechnique(_QuantBase):
                     x = stats[(i, name)].sample * self._awq_scale.get((i, name), 1.0)
                     ratio = methods.awq_clip(w, x, cfg.format, g, cfg.symmetric, cfg.awq_grid)
                     qw = methods.rtn(w, cfg.format, g, cfg.symmetric, ratio)
+                elif cfg.method == "hqq":
+                    qw = methods.hqq(w, cfg.format, cfg.group_size, cfg.symmetric, cfg.hqq_iters, cfg.hqq_p)
                 else:
                     qw = methods.rtn(w, cfg.format, cfg.group_size, cfg.symmetric)
                 self.weights[_key(i, name)] = qw
@@ -173,9 +175,14 @@ class QuantTechnique(_QuantBase):
             for name in names:
                 if name == "wo" and c.num_heads != c.num_kv_heads:
                     continue  # query heads share value heads: no per-channel producer to fold into
+                if cfg.method == "smoothquant" and name not in ("wqkv", "w_gate_up"):
+                    continue  # SmoothQuant smooths the inputs that a norm produces (QKV and the first FFN map)
                 w = getattr(layer, name)
-                s = methods.awq_search([w.detach()], stats[(i, name)], cfg.format, g or w.shape[1], cfg.symmetric,
-                                       cfg.awq_grid)
+                if cfg.method == "smoothquant":
+                    s = methods.smooth_scales([w.detach()], stats[(i, name)], cfg.smooth_alpha)
+                else:
+                    s = methods.awq_search([w.detach()], stats[(i, name)], cfg.format, g or w.shape[1],
+                                           cfg.symmetric, cfg.awq_grid)
                 w.mul_(s.to(w.dtype)[None, :])
                 if name == "wqkv":
                     layer.attn_norm.div_(s.to(layer.attn_norm.dtype))

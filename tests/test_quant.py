@@ -14,17 +14,17 @@ from economize_b200.techniques.quant.methods import collect
 from .helpers import gpu_tiny_model, prompts, reference_greedy, tiny_model
 
 
-@pytest.mark.parametrize("fmt", ["int4", "int8", "fp8"])
+@pytest.mark.parametrize("fmt", ["int2", "int3", "int4", "int8", "fp8"])
 def test_pack_roundtrip(fmt):
     g = torch.Generator().manual_seed(0)
-    if fmt == "int4":
-        codes = torch.randint(0, 16, (24, 128), generator=g)
+    if fmt in ("int2", "int3", "int4"):
+        codes = torch.randint(0, {"int2": 4, "int3": 8, "int4": 16}[fmt], (24, 128), generator=g)
     elif fmt == "int8":
         codes = torch.randint(-128, 128, (24, 128), generator=g)
     else:
         codes = (torch.randn(24, 128, generator=g) * 50).to(torch.float8_e4m3fn).float()
     packed = pack(codes, fmt)
-    assert packed.dtype == torch.uint8 and packed.shape == (24, 64 if fmt == "int4" else 128)
+    assert packed.dtype == torch.uint8 and packed.shape == (24, {"int2": 32, "int3": 64, "int4": 64}.get(fmt, 128))
     assert torch.equal(unpack(packed, fmt).to(codes.dtype), codes)
 
 
@@ -35,7 +35,7 @@ def test_int4_nibble_order():
 
 
 @pytest.mark.parametrize("fmt,sym,tol", [("int4", False, 0.12), ("int4", True, 0.13), ("int8", True, 0.009),
-                                         ("fp8", True, 0.04)])
+                                         ("fp8", True, 0.04), ("int3", False, 0.25), ("int2", False, 0.55)])
 def test_rtn_error(fmt, sym, tol):
     w = torch.randn(64, 256) * 0.02
     qw = rtn(w, fmt, 128, sym)
@@ -133,13 +133,13 @@ def test_config_checks():
 
 # ---- GPU ------------------------------------------------------------------------------------------------------
 @pytest.mark.gpu
-@pytest.mark.parametrize("fmt", ["int4", "int8", "fp8"])
+@pytest.mark.parametrize("fmt", ["int2", "int3", "int4", "int8", "fp8"])
 @pytest.mark.parametrize("M,N,K,group", [(1, 4096, 4096, 128), (61, 6144, 4096, 128), (7, 264, 512, 64),
                                          (200, 1024, 2048, 2048), (600, 512, 1024, 128)])
 def test_linear_wq_matches_fp32(cuda, fmt, M, N, K, group):
     g = torch.Generator(device=cuda).manual_seed(0)
     w = torch.randn(N, K, device=cuda, generator=g) * 0.02
-    qw = rtn(w, fmt, group, fmt != "int4")
+    qw = rtn(w, fmt, group, fmt not in ("int2", "int3", "int4"))
     x = torch.randn(M, K, device=cuda, generator=g).bfloat16()
     y = ops.linear(x, qw)
     exact = x.float() @ qw.dequantize(torch.float32).t()
@@ -213,3 +213,43 @@ def test_linear_fp8_matches_reference(cuda, M, N, K):
     err = (y.float() - exact).norm() / exact.norm()
     assert err < 1e-2, err
     torch.testing.assert_close(y.float(), exact, atol=8e-2, rtol=5e-2)
+
+
+def test_int2_word_layout():
+    codes = torch.arange(16).remainder(4).repeat(2, 1)  # k0..k15 = 0 1 2 3 0 1 2 3 ...
+    word = int.from_bytes(bytes(pack(codes, "int2")[0, :4].tolist()), "little")
+    assert [(word >> (2 * m)) & 3 for m in range(8)] == [int(c) for c in codes[0, 0::2]]
+    assert [(word >> (16 + 2 * m)) & 3 for m in range(8)] == [int(c) for c in codes[0, 1::2]]
+
+
+@pytest.mark.parametrize("fmt", ["int2", "int3"])
+def test_low_bit_models_decode(fmt):
+    em = eco.apply(tiny_model(), QuantConfig(format=fmt, method="rtn", group_size=64))
+    assert em.decode(prompts((10,))[0], 4).tokens.numel() == 4
+
+
+@pytest.mark.parametrize("fmt", ["int2", "int3", "int4"])
+def test_hqq_not_worse_than_rtn(fmt):
+    from economize_b200.techniques.quant.methods import hqq
+
+    g = torch.Generator().manual_seed(3)
+    w = torch.randn(64, 256, generator=g) * 0.02
+    w[:, ::37] *= 8  # heavy-tailed groups: the l_p error model helps here
+    e_rtn = (rtn(w, fmt, 64, False).dequantize(torch.float32) - w).norm()
+    e_hqq = (hqq(w, fmt, 64, False).dequantize(torch.float32) - w).norm()
+    assert e_hqq <= e_rtn * 1.0001, (float(e_hqq), float(e_rtn))
+
+
+def test_smoothquant_fp8_block_decodes_and_moves_outliers():
+    from economize_b200.techniques.quant.methods import _Stats, smooth_scales
+
+    st = _Stats(False, 64)
+    x = torch.randn(64, 8)
+    x[:, 3] *= 50
+    st.add(x)
+    s = smooth_scales([torch.randn(16, 8) * 0.02], st, 0.5)
+    assert int(s.argmax()) == 3
+    cal = torch.randint(0, 1024, (2, 32), generator=torch.Generator().manual_seed(2))
+    em = eco.apply(tiny_model(), QuantConfig(format="fp8_block", method="smoothquant", group_size=None),
+                   calibration=cal)
+    assert em.decode(prompts((10,))[0], 4).tokens.numel() == 4
