@@ -75,13 +75,21 @@ def fit(model, data: Any, objective: Objective | str | None = None, config: Trai
         torch.manual_seed(cfg.seed)
         random.seed(cfg.seed)
     obj = _objective(model, objective)
-    source = TensorSource(data, cfg.batch_size, seed=cfg.seed or 0) if isinstance(data, torch.Tensor) else data
+    dist_on = torch.distributed.is_available() and torch.distributed.is_initialized()
+    rank = torch.distributed.get_rank() if dist_on else 0
+    # data parallelism: every rank draws its own batches (the seed is offset by the rank)
+    source = TensorSource(data, cfg.batch_size, seed=(cfg.seed or 0) + 1000003 * rank) \
+        if isinstance(data, torch.Tensor) else data
     ckpt = RunCheckpointer(cfg.output_dir, cfg.keep_checkpoints) if cfg.output_dir is not None else None
     params = obj.parameters()
     if not params:
         raise ConfigError("the objective has no trainable parameters")
     modules = {id(p): p for p in params}
     orig_dtype = params[0].dtype
+    if dist_on:  # data parallelism: every rank starts from rank 0's parameters (as DDP does)
+        with torch.no_grad():
+            for p in params:
+                torch.distributed.broadcast(p.data, src=0)
     for p in params:  # fp32 master weights while training
         p.data = p.data.float()
     d = obj.defaults

@@ -1,0 +1,115 @@
+"""Training extras: data sources (token files, sharding, passkey), data-parallel fit over two Gloo ranks (each rank
+draws its own batches, parameters stay identical), and the Trainer integration's module and collator."""
+
+import os
+import socket
+
+import numpy as np
+import pytest
+import torch
+import torch.multiprocessing as mp
+
+import economize_b200 as eco
+from economize_b200.techniques.medusa import MedusaConfig
+from economize_b200.train.data import ShardedSource, TensorSource, TokenFileSource, passkey_prompts
+from economize_b200.train.trainer import EffCollator, ObjectiveModule
+
+from .helpers import tiny_model
+
+
+def test_token_file_source(tmp_path):
+    path = tmp_path / "tokens.bin"
+    np.arange(5000, dtype=np.uint16).tofile(path)
+    src = TokenFileSource(path, batch_size=3, seq_len=16, seed=1)
+    b = src.next()
+    assert b.shape == (3, 17) and bool(((b[:, 1:] - b[:, :-1]) == 1).all())
+    state = src.state()
+    nxt = src.next()
+    src.restore(state)
+    assert torch.equal(src.next(), nxt)
+
+
+def test_sharded_source_partitions_a_stream():
+    data = torch.arange(40).reshape(40, 1)
+    a = ShardedSource(TensorSource(data, 1, seed=0), 0, 2)
+    b = ShardedSource(TensorSource(data, 1, seed=0), 1, 2)
+    ref = TensorSource(data, 1, seed=0)
+    stream = [int(ref.next()) for _ in range(6)]
+    assert [int(a.next()) for _ in range(3)] == stream[0::2]
+    assert [int(b.next()) for _ in range(3)] == stream[1::2]
+
+
+def test_passkey_prompts():
+    p, k = passkey_prompts(3, 64, 1024, key_len=4, seed=0)
+    assert p.shape == (3, 64) and k.shape == (3, 4)
+    for i in range(3):
+        row = p[i].tolist()
+        assert any(row[j:j + 4] == k[i].tolist() for j in range(60)) and row[-1] == int(k[i, 0])
+
+
+def test_objective_module_and_collator():
+    em = eco.apply(tiny_model(), MedusaConfig(num_heads=2))
+    from economize_b200.train.objective import OBJECTIVES
+
+    mod = ObjectiveModule(OBJECTIVES.get("medusa_ce")(em))
+    batch = EffCollator()([{"input_ids": list(range(16))}, {"input_ids": list(range(16, 32))}])
+    out = mod(**batch)
+    out["loss"].backward()
+    assert batch["input_ids"].shape == (2, 16)
+    assert any(p.grad is not None for p in mod.parameters())
+    assert {id(p) for p in mod.parameters()} <= {id(p) for p in em.techniques["medusa"].parameters()}
+
+
+def _port() -> int:
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        return s.getsockname()[1]
+
+
+def _dp_worker(rank, port, queue):
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    import datetime
+
+    import torch.distributed as dist
+
+    dist.init_process_group("gloo", rank=rank, world_size=2, timeout=datetime.timedelta(seconds=60))
+    try:
+        em = eco.apply(tiny_model(), MedusaConfig(num_heads=2))
+        data = torch.randint(0, 1024, (64, 24), generator=torch.Generator().manual_seed(0))
+        seen = []
+        src = TensorSource(data, 4, seed=1000003 * rank)
+        orig = src.next
+
+        def record():
+            b = orig()
+            seen.append(b.clone())
+            return b
+
+        src.next = record
+        eco.train.fit(em, src, steps=3, batch_size=4, log_every=100)
+        flat = torch.cat([p.detach().flatten().float() for p in em.techniques["medusa"].parameters()])
+        other = flat.clone()
+        dist.broadcast(other, src=0)
+        queue.put((rank, bool(torch.equal(flat, other)), seen[0].sum().item()))
+    except Exception as err:
+        queue.put((rank, f"{type(err).__name__}: {err}", None))
+    finally:
+        dist.destroy_process_group()
+
+
+def test_data_parallel_fit_keeps_ranks_in_sync():
+    ctx = mp.get_context("spawn")
+    queue = ctx.Queue()
+    port = _port()
+    procs = [ctx.Process(target=_dp_worker, args=(r, port, queue)) for r in range(2)]
+    for p in procs:
+        p.start()
+    try:
+        res = dict((r, (same, s)) for r, same, s in (queue.get(timeout=180) for _ in procs))
+    finally:
+        for p in procs:
+            p.join(timeout=60)
+            if p.is_alive():
+                p.kill()
+    assert res[0][0] is True and res[1][0] is True, res
+    assert res[0][1] != res[1][1]  # the ranks drew different batches
