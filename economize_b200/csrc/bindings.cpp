@@ -1045,6 +1045,30 @@ int64_t status(int64_t device) {
   return static_cast<int64_t>(host);
 }
 
+// Failure-detection probe: the expert-parallel segments kernel of a one-rank buffer waits for a dispatch that nothing
+// sends; its bounded wait gives up after the device wait limit, sets the wait-peer status bit and returns. Returns the
+// status word (cleared unless keep_status).
+int64_t ep_wait_probe(int64_t ptr, int64_t experts_local, int64_t cap, int64_t hidden, int64_t ret_rows,
+                      bool keep_status) {
+  int device = 0;
+  cudaGetDevice(&device);
+  const at::Device dev(at::kCUDA, static_cast<c10::DeviceIndex>(device));
+  const ecz::EpLayout L = ecz::ep_layout(1, static_cast<int>(experts_local), static_cast<int>(cap),
+                                         static_cast<int>(hidden), static_cast<int>(ret_rows));
+  ecz::PeerPtrs peers{};
+  peers.ptr[0] = reinterpret_cast<void*>(ptr);
+  auto seg = at::empty({3, experts_local}, at::TensorOptions().dtype(at::kInt).device(dev));
+  int* s0 = seg.data_ptr<int>();
+  cudaStream_t stream = at::cuda::getCurrentCUDAStream();
+  TORCH_CHECK(ecz::launch_ep_segments(peers, L, 0, s0, s0 + experts_local, s0 + 2 * experts_local, status_word(dev),
+                                      stream) == 0, "ep_wait_probe: launch failed");
+  cudaStreamSynchronize(stream);
+  unsigned host = 0;
+  cudaMemcpy(&host, status_word(dev), sizeof(unsigned), cudaMemcpyDeviceToHost);
+  if (!keep_status && host != 0) cudaMemset(status_word(dev), 0, sizeof(unsigned));
+  return static_cast<int64_t>(host);
+}
+
 std::tuple<int64_t, int64_t, int64_t> attention_plan(int64_t B, int64_t T, int64_t H, int64_t Hkv, int64_t S,
                                                      int64_t sms) {
   const ecz::AttnPlan p = ecz::attention_plan(B, T, H, Hkv, S, sms);
@@ -1106,6 +1130,9 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("colsparse_linear", &colsparse_linear, "activation-sparse GEMV over a transposed weight (<= 16 rows)");
   m.def("glu_rows", &glu_rows, "gated-MLP hidden over the kept channels only (CATS / Deja Vu, <= 16 rows)");
   m.def("ep_buffer_bytes", &ep_buffer_bytes, "bytes of one rank's expert-parallel symmetric buffer");
+  m.def("ep_wait_probe", &ep_wait_probe, "run one bounded device wait that nothing satisfies; return the status",
+        py::arg("ptr"), py::arg("experts_local"), py::arg("cap"), py::arg("hidden"), py::arg("ret_rows"),
+        py::arg("keep_status") = false);
   m.def("ep_moe", &ep_moe, "expert-parallel MoE MLP with NVLink peer-store dispatch and combine");
   m.def("symm_alloc", &symm_alloc, "cudaMalloc an IPC-exportable buffer: (pointer, handle)");
   m.def("symm_open", &symm_open, "map a peer's buffer from its IPC handle");

@@ -69,3 +69,26 @@ def test_objectives_train(cfg, name):
         opt.step()
         losses.append(float(loss.detach()))
     assert min(losses[1:]) < losses[0], losses
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("make,decoding", [
+    (lambda m: HydraConfig(num_heads=3), None),
+    (lambda m: RedrafterConfig(beam_width=4, beam_length=3), None),
+    (lambda m: JumpConfig(target_layer=1, source_layer=1), None),
+    (lambda m: DFlashConfig(block_size=4), None),
+    (lambda m: PardConfig(model=m, max_drafts=3), None),
+])
+def test_lossless_on_gpu_with_graphs(cuda, make, decoding):
+    from .helpers import gpu_tiny_model
+
+    model = gpu_tiny_model(cuda)
+    ps = [p.to(cuda) for p in prompts((17, 33))]
+    plain = eco.apply(model).decode_batch(ps, 16, decoding=eco.DecodeConfig(cycle_length=1))
+    em = eco.apply(model, make(model))
+    base = decoding or em.decoding
+    import dataclasses
+
+    out = em.decode_batch(ps, 16, decoding=dataclasses.replace(base, cuda_graphs=True))
+    for a, b in zip(plain, out):
+        assert torch.equal(a.tokens.cpu(), b.tokens.cpu())
