@@ -74,3 +74,27 @@ def test_kangaroo_adapter_trains():
     after = list(eff.techniques["kangaroo"].adapter.parameters())
     assert any(not torch.equal(a, b) for a, b in zip(before, after))
     assert model.layers[1].wqkv is not eff.techniques["kangaroo"].adapter[0].wqkv
+
+
+@pytest.mark.parametrize("adaptation", ["lora", "full"])
+def test_early_exit_readout_adaptation_trains_and_stays_lossless(adaptation):
+    from economize_b200.techniques.early_exit import EarlyExitConfig
+    from economize_b200.train.objective import OBJECTIVES
+
+    model = tiny_model()
+    plain = eco.apply(model).decode_batch(prompts(), 16, decoding=eco.DecodeConfig(cycle_length=1))
+    em = eco.apply(model, EarlyExitConfig(exit_layer=2, adaptation=adaptation))
+    obj = OBJECTIVES.get("layerskip")(em)
+    cal = torch.randint(0, 1024, (2, 32), generator=torch.Generator().manual_seed(0))
+    opt = torch.optim.Adam(obj.parameters(), lr=3e-3)
+    losses = []
+    for _ in range(6):
+        loss, _ = obj.loss(cal)
+        opt.zero_grad()
+        loss.backward()
+        opt.step()
+        losses.append(float(loss.detach()))
+    assert losses[-1] < losses[0]
+    out = em.decode_batch(prompts(), 16, decoding=eco.DecodeConfig(cycle_length=4))
+    for a, b in zip(plain, out):
+        assert torch.equal(a.tokens, b.tokens)
