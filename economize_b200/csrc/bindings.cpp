@@ -893,6 +893,58 @@ Tensor glu_rows(Tensor x, Tensor w_gate_up, c10::optional<Tensor> gate, c10::opt
   return h.view(sizes);
 }
 
+// ---- draft trees (tree.cu) -------------------------------------------------------------------------------------
+// One depth of a dynamic-tree expansion (see tree.cu); every tensor is updated in place.
+void tree_expand(Tensor c_vals, Tensor c_ids, Tensor f_scores, Tensor f_cand, Tensor f_tokens, Tensor parent_fwd,
+                 Tensor fwd_bits, Tensor origin, Tensor bits_next, Tensor cand_tokens, Tensor cand_scores,
+                 Tensor cand_parents, int64_t d, bool next) {
+  CHECK_CUDA(c_vals);
+  TORCH_CHECK(c_vals.scalar_type() == at::kFloat && f_scores.scalar_type() == at::kFloat &&
+                  cand_scores.scalar_type() == at::kFloat, "tree_expand: fp32 scores");
+  for (const Tensor* t : {&c_ids, &f_cand, &f_tokens, &parent_fwd, &fwd_bits, &origin, &bits_next, &cand_tokens,
+                          &cand_parents}) {
+    TORCH_CHECK(t->scalar_type() == at::kLong && t->is_contiguous(), "tree_expand: contiguous int64 index tensors");
+    CHECK_ON(*t, c_vals);
+  }
+  CHECK_ON(f_scores, c_vals);
+  CHECK_ON(cand_scores, c_vals);
+  TORCH_CHECK(c_vals.is_contiguous() && f_scores.is_contiguous() && cand_scores.is_contiguous(),
+              "tree_expand: contiguous scores");
+  c10::cuda::CUDAGuard guard(c_vals.device());
+  const int B = static_cast<int>(f_scores.size(0)), k = static_cast<int>(f_scores.size(1));
+  TORCH_CHECK(c_vals.numel() == static_cast<int64_t>(B) * k * k, "tree_expand: c_vals [B, k, k]");
+  const int rc = ecz::launch_tree_expand(
+      c_vals.data_ptr<float>(), c_ids.data_ptr<int64_t>(), f_scores.data_ptr<float>(), f_cand.data_ptr<int64_t>(),
+      f_tokens.data_ptr<int64_t>(), parent_fwd.data_ptr<int64_t>(), fwd_bits.data_ptr<int64_t>(),
+      origin.data_ptr<int64_t>(), bits_next.data_ptr<int64_t>(), cand_tokens.data_ptr<int64_t>(),
+      cand_scores.data_ptr<float>(), cand_parents.data_ptr<int64_t>(), B, k, static_cast<int>(d),
+      static_cast<int>(cand_tokens.size(1)), static_cast<int>(fwd_bits.size(1)), next,
+      at::cuda::getCurrentCUDAStream());
+  TORCH_CHECK(rc == 0, "tree_expand: k <= 16 and (d + 1) k <= 64");
+}
+
+std::tuple<Tensor, Tensor> tree_select(Tensor cand_tokens, Tensor cand_scores, Tensor cand_parents, int64_t k,
+                                       int64_t total) {
+  CHECK_CUDA(cand_tokens);
+  CHECK_ON(cand_scores, cand_tokens);
+  CHECK_ON(cand_parents, cand_tokens);
+  TORCH_CHECK(cand_tokens.scalar_type() == at::kLong && cand_parents.scalar_type() == at::kLong &&
+                  cand_scores.scalar_type() == at::kFloat, "tree_select: int64 tokens / parents, fp32 scores");
+  c10::cuda::CUDAGuard guard(cand_tokens.device());
+  cand_tokens = cand_tokens.contiguous();
+  cand_scores = cand_scores.contiguous();
+  cand_parents = cand_parents.contiguous();
+  const int B = static_cast<int>(cand_tokens.size(0)), N = static_cast<int>(cand_tokens.size(1));
+  auto tokens = at::empty({B, total}, cand_tokens.options());
+  auto parents = at::empty({B, total}, cand_tokens.options());
+  const int rc = ecz::launch_tree_select(cand_tokens.data_ptr<int64_t>(), cand_scores.data_ptr<float>(),
+                                         cand_parents.data_ptr<int64_t>(), B, N, static_cast<int>(k),
+                                         static_cast<int>(total), tokens.data_ptr<int64_t>(),
+                                         parents.data_ptr<int64_t>(), at::cuda::getCurrentCUDAStream());
+  TORCH_CHECK(rc == 0, "tree_select: 1 <= total <= candidates <= 4096");
+  return {tokens, parents};
+}
+
 // ---- binary factors (binary.cu) ---------------------------------------------------------------------------------
 // x [M <= 16, K] fp32 times the sign matrix bits [N, ceil(K / 32)] (int32 words, bit set = -1) -> [M, N] fp32.
 Tensor sign_matvec(Tensor bits, Tensor x) {
@@ -1126,6 +1178,8 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("sample", &sample, "inverse-CDF draw of one token per probability row");
   m.def("rejection", &rejection, "lossless speculative sampling of a draft chain (accept/reject + resample)");
   m.def("ngram", &ngram, "prompt-lookup draft proposals from the token history");
+  m.def("tree_expand", &tree_expand, "one depth of dynamic-tree drafting bookkeeping (in place)");
+  m.def("tree_select", &tree_select, "the best candidates of a draft tree in candidate order, parents remapped");
   m.def("sign_matvec", &sign_matvec, "x times a packed sign matrix (LittleBit factors, <= 16 rows)");
   m.def("colsparse_linear", &colsparse_linear, "activation-sparse GEMV over a transposed weight (<= 16 rows)");
   m.def("glu_rows", &glu_rows, "gated-MLP hidden over the kept channels only (CATS / Deja Vu, <= 16 rows)");

@@ -155,6 +155,14 @@ int launch_glu_rows(const void* x, int ldx, const void* w, const void* gate_pre,
 // binary.cu: out[m, n] = sum_k s[n, k] x[m, k] with sign bits packed 32 per word along k (bit set = -1), M <= 16.
 int launch_sign_matvec(const uint32_t* bits, const float* x, float* out, int M, int N, int K, cudaStream_t stream);
 
+// tree.cu: dynamic-tree drafting bookkeeping (one CTA per row).
+int launch_tree_expand(const float* c_vals, const int64_t* c_ids, float* f_scores, int64_t* f_cand, int64_t* f_tokens,
+                       int64_t* parent_fwd, int64_t* fwd_bits, int64_t* origin, int64_t* bits_next,
+                       int64_t* cand_tokens, float* cand_scores, int64_t* cand_parents, int B, int k, int d,
+                       int n_cand, int n_fwd, bool next, cudaStream_t stream);
+int launch_tree_select(const int64_t* cand_tokens, const float* cand_scores, const int64_t* cand_parents, int B,
+                       int n_cand, int k, int total, int64_t* out_tokens, int64_t* out_parents, cudaStream_t stream);
+
 // ep.cu: expert-parallel dispatch / combine over IPC-mapped symmetric buffers (layout below, per rank).
 struct EpLayout {
   int world = 1, experts_local = 1, cap = 1, hidden = 8, ret_rows = 1;

@@ -148,6 +148,45 @@ struct Cand {
 
 __device__ __forceinline__ bool better(const Cand& a, const Cand& b) { return a.v > b.v || (a.v == b.v && a.i < b.i); }
 
+// Sorted (descending) candidate list of K entries kept in registers: insertion bubbles the new candidate down with
+// unrolled compare-and-swaps, and popping the head shifts the list (no dynamic indexing, so no local memory).
+template <int K>
+__device__ __forceinline__ void list_insert(Cand (&m)[K], Cand c) {
+  if (!better(c, m[K - 1])) return;
+#pragma unroll
+  for (int j = 0; j < K; ++j) {
+    if (better(c, m[j])) {
+      const Cand t = m[j];
+      m[j] = c;
+      c = t;
+    }
+  }
+}
+
+template <int K>
+__device__ __forceinline__ void list_pop(Cand (&m)[K]) {
+#pragma unroll
+  for (int j = 0; j < K - 1; ++j) m[j] = m[j + 1];
+  m[K - 1] = Cand{-INFINITY, 0x7fffffff};
+}
+
+// k rounds of the best head among the 32 lanes' sorted lists; lane 0 receives the k winners in order
+template <int K>
+__device__ __forceinline__ void warp_merge(Cand (&m)[K], int k, Cand* out) {
+  for (int r = 0; r < k; ++r) {
+    const Cand c = m[0];
+    Cand best = c;
+#pragma unroll
+    for (int off = 16; off > 0; off >>= 1) {
+      const Cand o{__shfl_xor_sync(0xffffffffu, best.v, off), __shfl_xor_sync(0xffffffffu, best.i, off)};
+      if (better(o, best)) best = o;
+    }
+    if (c.i == best.i && c.v == best.v) list_pop(m);
+    if ((threadIdx.x & 31) == 0) out[r] = best;
+  }
+}
+
+template <int K>
 __global__ void __launch_bounds__(kTopThreads) topk_logp_kernel(const float* __restrict__ logits,
                                                                const int64_t* __restrict__ d2t, float* __restrict__ vals,
                                                                int64_t* __restrict__ ids, int V, int k, float floor_v) {
@@ -156,66 +195,49 @@ __global__ void __launch_bounds__(kTopThreads) topk_logp_kernel(const float* __r
   const float* row = logits + static_cast<size_t>(blockIdx.x) * V;
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   __shared__ float red[32];
-  __shared__ Cand wl[kTopThreads / 32][kMaxTopK];
-  // max
-  float mx = -INFINITY;
-  for (int i = tid; i < V; i += kTopThreads) mx = fmaxf(mx, row[i]);
-  mx = warp_max(mx);
-  if (lane == 0) red[warp] = mx;
-  __syncthreads();
-  if (warp == 0) {
-    float t = lane < kTopThreads / 32 ? red[lane] : -INFINITY;
-    t = warp_max(t);
-    if (lane == 0) red[0] = t;
-  }
-  __syncthreads();
-  mx = red[0];
-  __syncthreads();
-  // sum of exponentials and the thread's own top-k (sorted, descending)
-  Cand mine[kMaxTopK];
-  for (int j = 0; j < k; ++j) mine[j] = {-INFINITY, 0x7fffffff};
-  float se = 0.f;
+  __shared__ Cand wl[kTopThreads / 32][K];
+  // one pass: the thread's running max with a rescaled sum of exponentials, and its own top-K
+  Cand mine[K];
+#pragma unroll
+  for (int j = 0; j < K; ++j) mine[j] = Cand{-INFINITY, 0x7fffffff};
+  float mx = -INFINITY, se = 0.f;
   for (int i = tid; i < V; i += kTopThreads) {
-    const float x = row[i];
-    se += __expf(x - mx);
-    Cand c{x, i};
-    if (better(c, mine[k - 1])) {
-      int j = k - 1;
-      while (j > 0 && better(c, mine[j - 1])) {
-        mine[j] = mine[j - 1];
-        --j;
-      }
-      mine[j] = c;
+    const float x = __ldg(row + i);
+    if (x > mx) {
+      se = se * __expf(mx - x) + 1.f;
+      mx = x;
+    } else if (x != -INFINITY) {  // a -inf logit adds nothing (and exp(-inf - -inf) would be NaN)
+      se += __expf(x - mx);
     }
+    list_insert(mine, Cand{x, i});
   }
-  se = warp_sum(se);
-  if (lane == 0) red[warp] = se;
-  // warp merge: k rounds of the best head among the 32 lanes' lists
-  int head = 0;
-  for (int r = 0; r < k; ++r) {
-    Cand c = head < k ? mine[head] : Cand{-INFINITY, 0x7fffffff};
-    Cand best = c;
-    for (int off = 16; off > 0; off >>= 1) {
-      Cand o{__shfl_xor_sync(0xffffffffu, best.v, off), __shfl_xor_sync(0xffffffffu, best.i, off)};
-      if (better(o, best)) best = o;
-    }
-    if (head < k && c.i == best.i && c.v == best.v) ++head;
-    if (lane == 0) wl[warp][r] = best;
+  // block log-sum-exp: warp-level then block-level (max, rescaled sum)
+  float wmx = warp_max(mx);
+  float wse = warp_sum(mx == -INFINITY ? 0.f : se * __expf(mx - wmx));
+  if (lane == 0) {
+    red[warp] = wmx;
+    red[16 + warp] = wse;
   }
+  warp_merge(mine, k, wl[warp]);
   __syncthreads();
   if (warp == 0) {
-    float tot = lane < kTopThreads / 32 ? red[lane] : 0.f;
-    tot = warp_sum(tot);
-    const float lse = mx + __logf(tot);
-    int h = 0;  // lane l merges list l (16 lists of k)
+    const float m_l = lane < kTopThreads / 32 ? red[lane] : -INFINITY;
+    const float bmx = warp_max(m_l);
+    const float s_l = lane < kTopThreads / 32 && m_l != -INFINITY ? red[16 + lane] * __expf(m_l - bmx) : 0.f;
+    const float lse = bmx + __logf(warp_sum(s_l));
+    // lane l holds warp l's sorted list (16 lists of k)
+    Cand lst[K];
+#pragma unroll
+    for (int j = 0; j < K; ++j) lst[j] = (lane < kTopThreads / 32 && j < k) ? wl[lane][j] : Cand{-INFINITY, 0x7fffffff};
     for (int r = 0; r < k; ++r) {
-      Cand c = (lane < kTopThreads / 32 && h < k) ? wl[lane][h] : Cand{-INFINITY, 0x7fffffff};
+      const Cand c = lst[0];
       Cand best = c;
+#pragma unroll
       for (int off = 16; off > 0; off >>= 1) {
-        Cand o{__shfl_xor_sync(0xffffffffu, best.v, off), __shfl_xor_sync(0xffffffffu, best.i, off)};
+        const Cand o{__shfl_xor_sync(0xffffffffu, best.v, off), __shfl_xor_sync(0xffffffffu, best.i, off)};
         if (better(o, best)) best = o;
       }
-      if (lane < kTopThreads / 32 && h < k && c.i == best.i && c.v == best.v) ++h;
+      if (c.i == best.i && c.v == best.v) list_pop(lst);
       if (lane == 0) {
         const size_t o = static_cast<size_t>(blockIdx.x) * k + r;
         vals[o] = fmaxf(best.v - lse, floor_v);
@@ -244,7 +266,14 @@ int launch_topk_logp(const float* logits, const int64_t* d2t, float* vals, int64
                      float floor_v, cudaStream_t stream) {
   if (k < 1 || k > kMaxTopK || k > V) return -1;
   if (rows == 0) return 0;
-  launch_pdl(topk_logp_kernel, dim3(rows), dim3(kTopThreads), 0, stream, logits, d2t, vals, ids, V, k, floor_v);
+  if (k <= 4) {
+    launch_pdl(topk_logp_kernel<4>, dim3(rows), dim3(kTopThreads), 0, stream, logits, d2t, vals, ids, V, k, floor_v);
+  } else if (k <= 8) {
+    launch_pdl(topk_logp_kernel<8>, dim3(rows), dim3(kTopThreads), 0, stream, logits, d2t, vals, ids, V, k, floor_v);
+  } else {
+    launch_pdl(topk_logp_kernel<16>, dim3(rows), dim3(kTopThreads), 0, stream, logits, d2t, vals, ids, V, k,
+               floor_v);
+  }
   return 0;
 }
 

@@ -510,6 +510,8 @@ class SpecEngine:
             vals, ids = ops.topk_logp(logits, k, LOGP_FLOOR, d2t)
             return vals, (ids if d2t is not None else drafter.to_target(ids))
 
+        if dev.type == "cuda":
+            return self._draft_tree_fused(st, expand)
         f_scores, f_tokens = expand(st.root_logits)  # frontier tokens [B, k]
         f_cand = torch.arange(k, device=dev).expand(batch, k)
         cand_tokens, cand_scores = [f_tokens], [f_scores]
@@ -549,3 +551,43 @@ class SpecEngine:
         parents = torch.cat(cand_parents, 1)
         depth_of = torch.cat(cand_depth)
         return select_candidates(tokens, scores, parents, depth_of, tree.total_tokens)
+
+    def _draft_tree_fused(self, st: _State, expand) -> tuple[torch.Tensor, torch.Tensor]:
+        """:meth:`_draft_tree` with the per-depth bookkeeping and the final selection in two CUDA kernels
+        (``csrc/tree.cu``): the same candidates, frontiers, ancestor bits and tree, far fewer launches."""
+        from ..ops._ext import require
+
+        C = require()
+        drafter, tree = self.drafter, self.tree
+        batch, dev = st.batch, st.kv_len.device
+        k, depth = tree.topk, tree.depth
+        n_cand = k + (depth - 1) * k * k
+        cand_tokens = torch.empty(batch, n_cand, dtype=torch.int64, device=dev)
+        cand_scores = torch.empty(batch, n_cand, dtype=torch.float32, device=dev)
+        cand_parents = torch.empty(batch, n_cand, dtype=torch.int64, device=dev)
+        f_scores, f_tokens = expand(st.root_logits)
+        f_scores = f_scores.contiguous()
+        f_tokens = f_tokens.contiguous()
+        cand_tokens[:, :k] = f_tokens
+        cand_scores[:, :k] = f_scores
+        cand_parents[:, :k] = -1
+        f_cand = torch.arange(k, device=dev).expand(batch, k).contiguous()
+        parent_fwd = torch.full((batch, k), -1, dtype=torch.int64, device=dev)
+        fwd_bits = torch.zeros(batch, max(tree.forwarded, 1), dtype=torch.int64, device=dev)
+        origin = torch.zeros(batch, k, dtype=torch.int64, device=dev)
+        bits = (torch.ones(batch, k, dtype=torch.int64, device=dev) << torch.arange(k, device=dev)[None]).contiguous()
+        fwd_bits[:, :k] = bits
+        states = st.root_state[:, None].expand(batch, k, st.root_state.shape[-1]).contiguous()
+        base = st.kv_len + 1
+        for d in range(1, depth):
+            pos = (st.kv_len + d).to(torch.int32)[:, None].expand(batch, k).contiguous()
+            logits, outs = drafter.tree_step(f_tokens, states, pos, base, d * k, (d - 1) * k, bits)
+            c_vals, c_ids = expand(logits)
+            nxt = d < depth - 1
+            new_bits = torch.empty_like(bits)
+            C.tree_expand(c_vals.contiguous(), c_ids.contiguous(), f_scores, f_cand, f_tokens, parent_fwd, fwd_bits,
+                          origin, new_bits, cand_tokens, cand_scores, cand_parents, d, nxt)
+            if nxt:
+                bits = new_bits
+                states = outs.gather(1, origin[..., None].expand(batch, k, outs.shape[-1]))
+        return C.tree_select(cand_tokens, cand_scores, cand_parents, k, tree.total_tokens)

@@ -306,3 +306,55 @@ def test_chunked_prefill_matches_whole_prefill(cuda):
     chunked = eco.apply(model).decode_batch(p, 12, decoding=eco.DecodeConfig(cycle_length=1, prefill_chunk=128))
     for a, b in zip(whole, chunked):
         assert torch.equal(a.tokens.cpu(), b.tokens.cpu())
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("k,depth,total", [(10, 6, 60), (4, 3, 16), (8, 4, 40)])
+def test_fused_tree_kernels_match_the_reference(cuda, k, depth, total):
+    """tree_expand + tree_select against the tensor operations of the engine's reference tree drafting."""
+    from economize_b200.decoding.tree import select_candidates
+    from economize_b200.ops._ext import require
+
+    C = require()
+    g = torch.Generator(device=cuda).manual_seed(k)
+    B = 3
+    n_cand = k + (depth - 1) * k * k
+    f_scores = -torch.rand(B, k, device=cuda, generator=g)
+    f_tokens = torch.randint(0, 1000, (B, k), device=cuda, generator=g)
+    cand_t = torch.empty(B, n_cand, dtype=torch.int64, device=cuda)
+    cand_s = torch.empty(B, n_cand, device=cuda)
+    cand_p = torch.empty(B, n_cand, dtype=torch.int64, device=cuda)
+    cand_t[:, :k], cand_s[:, :k], cand_p[:, :k] = f_tokens, f_scores, -1
+    ref_t, ref_s, ref_p, ref_d = [f_tokens.clone()], [f_scores.clone()], [torch.full((B, k), -1, device=cuda)], \
+        [torch.zeros(k, device=cuda)]
+    f_cand = torch.arange(k, device=cuda).expand(B, k).contiguous()
+    rf_cand, rf_scores = f_cand.clone(), f_scores.clone()
+    parent_fwd = torch.full((B, k), -1, dtype=torch.int64, device=cuda)
+    fwd_bits = torch.zeros(B, (depth - 1) * k, dtype=torch.int64, device=cuda)
+    fwd_bits[:, :k] = 1 << torch.arange(k, device=cuda)
+    origin = torch.zeros(B, k, dtype=torch.int64, device=cuda)
+    for d in range(1, depth):
+        c_vals = -torch.rand(B, k, k, device=cuda, generator=g) * 3
+        c_ids = torch.randint(0, 1000, (B, k, k), device=cuda, generator=g)
+        nb = torch.empty(B, k, dtype=torch.int64, device=cuda)
+        C.tree_expand(c_vals, c_ids, f_scores, f_cand, f_tokens, parent_fwd, fwd_bits, origin, nb, cand_t, cand_s,
+                      cand_p, d, d < depth - 1)
+        child_scores = (rf_scores[:, :, None] + c_vals).reshape(B, k * k)
+        ref_t.append(c_ids.reshape(B, k * k))
+        ref_s.append(child_scores)
+        ref_p.append(rf_cand[:, :, None].expand(B, k, k).reshape(B, k * k))
+        ref_d.append(torch.full((k * k,), float(d), device=cuda))
+        if d < depth - 1:
+            pick = child_scores.topk(k, -1).indices
+            rf_scores = child_scores.gather(1, pick)
+            rf_cand = k + (d - 1) * k * k + pick
+            assert torch.equal(f_cand, rf_cand) and torch.allclose(f_scores, rf_scores)
+            assert torch.equal(origin, pick // k)
+            assert torch.equal(nb, (1 << (d * k + torch.arange(k, device=cuda)))[None] |
+                               fwd_bits.gather(1, (d - 1) * k + pick // k))
+    assert torch.equal(cand_t, torch.cat(ref_t, 1)) and torch.equal(cand_p, torch.cat(ref_p, 1))
+    torch.testing.assert_close(cand_s, torch.cat(ref_s, 1))
+    tok, par = C.tree_select(cand_t, cand_s, cand_p, k, total)
+    rtok, rpar = select_candidates(torch.cat(ref_t, 1), torch.cat(ref_s, 1), torch.cat(ref_p, 1), torch.cat(ref_d),
+                                   total)
+    assert torch.equal(tok, rtok) and torch.equal(par, rpar)
