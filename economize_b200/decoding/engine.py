@@ -30,7 +30,9 @@ from ..runtime.cache import KVCache, StepBatch
 from ..runtime.phase import phase
 from .config import DecodeConfig
 from .drafter import DraftModel
-from .policies import POLICIES, ConfidencePolicy, DynamicTreePolicy
+from .policies import POLICIES, ConfidencePolicy, DynamicTreePolicy, SequoiaPolicy, SpecExecPolicy
+from .sequoia import AcceptanceProfile, StaticPlan, StaticTree, record_cycle
+from .specexec import SearchOptions
 from .tree import LOGP_FLOOR, TreeOptions, ancestor_bits, popcount64, select_candidates
 from .verifiers import VERIFIERS, RejectionVerifier, TypicalVerifier
 
@@ -125,12 +127,26 @@ class SpecEngine:
         self.verifier = VERIFIERS.get(config.verifier_name)(config)
         self.policy = POLICIES.get(config.draft_policy_name)(config)
         self.accept_all = config.verifier_name == "accept_all"
-        self.tree: TreeOptions | None = None
-        if self.drafter is not None and isinstance(self.policy, DynamicTreePolicy):
+        self.tree: TreeOptions | None = None  # EAGLE-2 dynamic trees
+        self.static_tree: StaticTree | None = None  # Sequoia
+        self.search: SearchOptions | None = None  # SpecExec
+        self.acceptance: AcceptanceProfile | None = None
+        self._plans: dict[torch.device, StaticPlan] = {}
+        if self.drafter is not None and self.policy.drafts_tree:
             if not self.verifier.supports_trees or self.verifier.needs_draft_probs:
-                raise ConfigError(f"draft_policy 'dynamic_tree' drafts trees, which verifier "
+                raise ConfigError(f"draft_policy {config.draft_policy_name!r} drafts trees, which verifier "
                                   f"{config.verifier_name!r} cannot verify; use greedy or typical")
-            self.tree = self.policy.options
+            if isinstance(self.policy, DynamicTreePolicy):
+                self.tree = self.policy.options
+            else:
+                if hasattr(self.drafter, "propose"):
+                    raise ConfigError(f"draft_policy {config.draft_policy_name!r} needs a drafter with tree steps; "
+                                      f"{type(self.drafter).__name__} proposes its own drafts")
+                if isinstance(self.policy, SequoiaPolicy):
+                    self.static_tree = self.policy.tree
+                    self.acceptance = AcceptanceProfile() if self.policy.record else None
+                elif isinstance(self.policy, SpecExecPolicy):
+                    self.search = self.policy.options
         self.rejection = isinstance(self.verifier, RejectionVerifier) and self.selector is not None
         self.min_confidence = self.policy.min_confidence if isinstance(self.policy, ConfidencePolicy) else None
         self.static = self.drafter is not None and hasattr(self.drafter, "propose")
@@ -144,9 +160,17 @@ class SpecEngine:
         elif self.tree is not None:
             self.depth = self.tree.depth
             self.nodes = self.tree.total_tokens
+        elif self.static_tree is not None:
+            self.depth = self.static_tree.depth
+            self.nodes = self.static_tree.size
+        elif self.search is not None:
+            self.depth = self.search.depth
+            self.nodes = self.search.total_tokens
         else:
             self.depth = config.cycle_length - 1
             self.nodes = self.depth
+        shape = self.tree or self.static_tree or self.search
+        self.forwarded = shape.forwarded if shape is not None else self.depth
         self._states: dict[tuple[int, int, int], _State] = {}
         self._graphs: dict[tuple[int, int, int], torch.cuda.CUDAGraph] = {}
         self.stats = GenerationStats()
@@ -157,7 +181,7 @@ class SpecEngine:
         return self.depth + 1
 
     def capacity_for(self, prompt_len: int, max_new: int) -> int:
-        slack = self.nodes + 2 + self.depth + (self.tree.forwarded if self.tree else self.depth) + 8
+        slack = self.nodes + 2 + self.depth + self.forwarded + 8
         return int(math.ceil((prompt_len + max_new + slack) / 128) * 128)
 
     @torch.no_grad()
@@ -278,7 +302,7 @@ class SpecEngine:
     def _run_cycles(self, st: _State, max_new: int, stop_tokens: list[int] | None) -> None:
         # drafters that search host-side structures (retrieval, suffix trees) synchronise with the host every cycle
         use_graph = self.config.cuda_graphs and self.model.device.type == "cuda" and \
-            getattr(self.drafter, "graph_safe", True)
+            getattr(self.drafter, "graph_safe", True) and self.acceptance is None
         key = (st.batch, st.capacity, st.out_cap)
         remaining = max_new - 1  # the prefill produced the first token
         per_cycle = self.tokens_per_cycle
@@ -347,6 +371,10 @@ class SpecEngine:
                 draft_tokens, draft_parents = drafter.propose(st.history, st.kv_len + 1)
             elif self.tree is not None:
                 draft_tokens, draft_parents = self._draft_tree(st)
+            elif self.static_tree is not None:
+                draft_tokens, draft_parents = self._draft_static_tree(st)
+            elif self.search is not None:
+                draft_tokens, draft_parents = self._draft_search(st)
             else:
                 draft_tokens, draft_parents, q_full = self._draft_chain(st)
             overlay = getattr(drafter, "overlay", None)  # a hybrid lays its primary's proposals over the drafts
@@ -364,6 +392,8 @@ class SpecEngine:
         with phase("refresh"):
             hidden, aux = model.forward_step(tokens.clamp_min(0), sb, st.cache, drafter.capture_layers)
         n_acc, path, out = self._verify(tokens, parents, hidden, draft_tokens, q_full)
+        if self.acceptance is not None:  # Sequoia rate measurement: one host synchronization per cycle
+            record_cycle(self.acceptance, self.static_tree, self._plan(dev), tokens, path, n_acc, out)
         ops.kv_compact(st.cache.data, st.kv_len, path, n_acc)
         # ---- commit ----
         active = st.n_out < st.max_new
@@ -591,3 +621,98 @@ class SpecEngine:
                 bits = new_bits
                 states = outs.gather(1, origin[..., None].expand(batch, k, outs.shape[-1]))
         return C.tree_select(cand_tokens, cand_scores, cand_parents, k, tree.total_tokens)
+
+    # ---- Sequoia static trees and SpecExec search -------------------------------------------------------------
+    def _plan(self, device: torch.device) -> StaticPlan:
+        plan = self._plans.get(device)
+        if plan is None:  # built by the eager warm-up cycles, before any graph capture
+            plan = self._plans[device] = StaticPlan(self.static_tree, device)
+        return plan
+
+    def _topk_ids(self, logits: torch.Tensor, k: int) -> torch.Tensor:
+        """Target ids of the ``k`` most likely draft tokens of every row of ``logits [..., V_d]``."""
+        d2t = getattr(self.drafter, "d2t_map", None)
+        if k <= 16:
+            _, ids = ops.topk_logp(logits, k, LOGP_FLOOR, d2t)
+            return ids if d2t is not None else self.drafter.to_target(ids)
+        return self.drafter.to_target(logits.topk(k, -1).indices)
+
+    def _draft_static_tree(self, st: _State) -> tuple[torch.Tensor, torch.Tensor]:
+        """Fill the Sequoia tree: every node is its parent's ``rank``-th most likely token; one draft step per depth
+        over the nodes of that depth with children (economize ``decoding/sequoia.py:SequoiaDrafter.propose``)."""
+        drafter, plan = self.drafter, self._plan(st.kv_len.device)
+        batch = st.batch
+        level = self._topk_ids(st.root_logits, plan.k[0])[:, plan.pick[0]]
+        levels = [level]
+        outs = None
+        base = st.kv_len + 1
+        for L in range(1, plan.depth):
+            width, offset = plan.widths[L - 1], plan.offset[L - 1]
+            tok = level[:, plan.fwd[L - 1]].contiguous()
+            if L == 1:
+                states = st.root_state[:, None].expand(batch, width, st.root_state.shape[-1]).contiguous()
+            else:
+                states = outs[:, plan.fwd_parent[L - 1]].contiguous()
+            pos = (st.kv_len + L).to(torch.int32)[:, None].expand(batch, width).contiguous()
+            bits = plan.bits[L - 1].expand(batch, width).contiguous()
+            logits, outs = drafter.tree_step(tok, states, pos, base, offset + width, offset, bits)
+            level = self._topk_ids(logits, plan.k[L]).reshape(batch, -1)[:, plan.pick[L]]
+            levels.append(level)
+        return torch.cat(levels, 1), plan.parents.expand(batch, plan.size)
+
+    def _draft_search(self, st: _State) -> tuple[torch.Tensor, torch.Tensor]:
+        """SpecExec: ``depth - 1`` best-first expansions of the ``width`` best open candidates, then the
+        ``total_tokens`` best candidates (economize ``decoding/specexec.py:SpecExecDrafter``)."""
+        drafter, opt = self.drafter, self.search
+        batch, dev = st.batch, st.kv_len.device
+        k, w = opt.topk, opt.width
+        log_decay = math.log(opt.decay)
+        d2t = getattr(drafter, "d2t_map", None)
+
+        def expand(logits: torch.Tensor) -> tuple[torch.Tensor, torch.Tensor]:
+            vals, ids = ops.topk_logp(logits, k, LOGP_FLOOR, d2t)
+            return vals, (ids if d2t is not None else drafter.to_target(ids))
+
+        n = opt.candidates
+        tokens = torch.empty(batch, n, dtype=torch.int64, device=dev)
+        scores = torch.empty(batch, n, dtype=torch.float32, device=dev)
+        parents = torch.empty(batch, n, dtype=torch.int64, device=dev)
+        depth = torch.empty(batch, n, dtype=torch.int64, device=dev)
+        slot_of = torch.empty(batch, n, dtype=torch.int64, device=dev)  # forwarded slot of a candidate, -1: open
+        vals, ids = expand(st.root_logits)
+        tokens[:, :k] = ids
+        scores[:, :k] = vals + log_decay
+        parents[:, :k] = -1
+        depth[:, :k] = 1
+        slot_of[:, :k] = -1
+        states = torch.empty(batch, 1 + opt.forwarded, st.root_state.shape[-1], dtype=st.root_state.dtype,
+                             device=dev)
+        states[:, 0] = st.root_state
+        fwd_bits = torch.zeros(batch, opt.forwarded, dtype=torch.int64, device=dev)
+        rows = torch.arange(batch, device=dev)[:, None]
+        lanes = torch.arange(w, device=dev)
+        base = st.kv_len + 1
+        filled = k
+        for s in range(opt.steps):
+            pick = torch.where(slot_of[:, :filled] >= 0, float("-inf"), scores[:, :filled]).topk(w, -1).indices
+            slot = s * w + lanes
+            par = parents.gather(1, pick)
+            par_slot = torch.where(par >= 0, slot_of.gather(1, par.clamp_min(0)), -1)
+            inherited = torch.where(par_slot >= 0, fwd_bits.gather(1, par_slot.clamp_min(0)), 0)
+            bits = (torch.ones(w, dtype=torch.int64, device=dev) << slot)[None] | inherited
+            fwd_bits[:, s * w:(s + 1) * w] = bits
+            slot_of.scatter_(1, pick, slot.expand(batch, w))
+            node_depth = depth.gather(1, pick)
+            pos = (st.kv_len[:, None] + node_depth).to(torch.int32)
+            logits, outs = drafter.tree_step(tokens.gather(1, pick), states[rows, par_slot + 1].contiguous(), pos,
+                                             base, (s + 1) * w, s * w, bits)
+            states[:, 1 + s * w:1 + (s + 1) * w] = outs
+            c_vals, c_ids = expand(logits)
+            lo, hi = filled, filled + w * k
+            tokens[:, lo:hi] = c_ids.reshape(batch, w * k)
+            scores[:, lo:hi] = (scores.gather(1, pick)[:, :, None] + c_vals + log_decay).reshape(batch, w * k)
+            parents[:, lo:hi] = pick[:, :, None].expand(batch, w, k).reshape(batch, w * k)
+            depth[:, lo:hi] = (node_depth + 1)[:, :, None].expand(batch, w, k).reshape(batch, w * k)
+            slot_of[:, lo:hi] = -1
+            filled = hi
+        return select_candidates(tokens, scores, parents, depth, opt.total_tokens)

@@ -6,6 +6,8 @@
   draft is always made). The engine keeps its shapes fixed: drafts after the stop are invalidated, so they are
   never accepted and the acceptance statistics are those of the shortened chain.
 * ``dynamic_tree``: EAGLE-2 dynamic trees (``depth``, ``topk``, ``total_tokens``).
+* ``sequoia``: one static tree of the best shape for measured acceptance rates (economize ``decoding/sequoia.py``).
+* ``specexec``: SpecExec best-first search over a candidate pool (economize ``decoding/specexec.py``).
 """
 
 from __future__ import annotations
@@ -16,7 +18,8 @@ from ..errors import ConfigError
 from ..registry import Registry
 from .tree import TreeOptions
 
-__all__ = ["POLICIES", "ConfidencePolicy", "DraftPolicy", "DynamicTreePolicy", "FixedPolicy"]
+__all__ = ["POLICIES", "ConfidencePolicy", "DraftPolicy", "DynamicTreePolicy", "FixedPolicy", "SequoiaPolicy",
+           "SpecExecPolicy"]
 
 
 class DraftPolicy:
@@ -54,3 +57,33 @@ class DynamicTreePolicy(DraftPolicy):
     def __init__(self, config: Any) -> None:
         super().__init__(config)
         self.options = TreeOptions.from_options(config.draft_policy_options, config.cycle_length)
+
+
+@POLICIES.register("sequoia")
+class SequoiaPolicy(DraftPolicy):
+    """One static Sequoia tree per cycle (options: ``acceptance`` or ``paths``, ``total_tokens``, ``depth``,
+    ``verify_latency``, ``draft_latency``, ``record_acceptance``; :mod:`economize_b200.decoding.sequoia`)."""
+
+    name = "sequoia"
+    drafts_tree = True
+
+    def __init__(self, config: Any) -> None:
+        from .sequoia import tree_from_options
+
+        super().__init__(config)
+        self.tree, self.record = tree_from_options(config.draft_policy_options, config.cycle_length)
+
+
+@POLICIES.register("specexec")
+class SpecExecPolicy(DraftPolicy):
+    """SpecExec best-first search (options: ``depth``, ``width``, ``topk``, ``total_tokens``, ``decay``;
+    :mod:`economize_b200.decoding.specexec`)."""
+
+    name = "specexec"
+    drafts_tree = True
+
+    def __init__(self, config: Any) -> None:
+        from .specexec import SearchOptions
+
+        super().__init__(config)
+        self.options = SearchOptions.from_options(config.draft_policy_options, config.cycle_length)

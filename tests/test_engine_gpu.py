@@ -111,3 +111,21 @@ def test_ngram_kernel(cuda):
         want = reference.ngram(hist, length, 5, 1, 3, earliest)
         got = eco.ops.ngram(hist.to(cuda), length.to(cuda), 5, 1, 3, earliest)
         assert torch.equal(got.cpu(), want)
+
+
+@pytest.mark.parametrize("policy,options", [
+    ("sequoia", {"acceptance": (0.6, 0.15, 0.06, 0.03), "total_tokens": 32, "depth": 6}),
+    ("specexec", {"depth": 6, "width": 8, "topk": 8, "total_tokens": 48}),
+])
+def test_tree_policies_are_greedy_and_graph_stable(em, cuda, policy, options):
+    """Sequoia static trees and SpecExec search on the CUDA path: greedy up to rounding, and the captured cycle
+    reproduces the eager one."""
+    prompts = _prompts(cuda)
+    base = dict(cycle_length=7, draft_policy=policy, draft_policy_options=options)
+    eager = em.decode_batch(prompts, 40, decoding=eco.DecodeConfig(**base))
+    graphed = em.decode_batch(prompts, 40, decoding=eco.DecodeConfig(**base, cuda_graphs=True))
+    for p, a, b in zip(prompts, eager, graphed):
+        assert a.tokens.numel() == 40
+        _assert_greedy(em, p, a.tokens)
+        assert torch.equal(a.tokens, b.tokens)
+    assert eco.ops.require().status(0) == 0
