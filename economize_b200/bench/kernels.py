@@ -8,7 +8,8 @@ peaks. Ops:
 * ``gemm``       bf16 ``x[M, K] @ w[N, K]^T`` (tcgen05 swap-AB GEMM vs cuBLAS through torch.matmul); calls on
   rotating weight copies (more than 2x L2 in total) are captured in one CUDA graph, so the per-call time excludes
   launch overhead and reads the weights from HBM
-* ``gemm_wq``    weight-only int4 / int8 / fp8 GEMM (``--fmt``), vs the bf16 kernel on the same shape
+* ``gemm_wq``    weight-only int2 / int4 / int8 / fp8 / mxfp4 / nvfp4 GEMM (``--fmt``), vs the bf16 kernel on the
+  same shape
 * ``attention``  tree-masked decode attention over a bf16 slot cache (``--tree`` new tokens per row)
 * ``layer``      one Llama-3.1-8B decoder layer's projections as a CUDA graph (``--tp`` shard), ours vs cuBLAS
 * ``teal``       activation-sparse GEMV (``colsparse_linear`` over a transposed weight) at ``--sparsity`` of the
@@ -79,12 +80,12 @@ def bench_gemm_wq(a) -> None:
     dev = torch.device("cuda")
     x = torch.randn(a.m, a.k, device=dev).bfloat16()
     w = torch.randn(a.n, a.k, device=dev) * 0.02
-    qw0 = rtn(w, a.fmt, a.group, a.fmt != "int4")
+    qw0 = rtn(w, a.fmt, a.group, a.fmt not in ("int2", "int4"))
     if a.once:
         ops.linear(x, qw0)
         torch.cuda.synchronize()
         return
-    qws = [qw0] + [rtn(w, a.fmt, a.group, a.fmt != "int4") for _ in range(_copies(qw0.nbytes()) - 1)]
+    qws = [qw0] + [rtn(w, a.fmt, a.group, a.fmt not in ("int2", "int4")) for _ in range(_copies(qw0.nbytes()) - 1)]
     wbs = [w.bfloat16() for _ in range(_copies(2 * a.n * a.k))]
     ours = time_graph([lambda q=q: ops.linear(x, q) for q in qws], a.iters, a.warmup)
     bf16 = time_graph([lambda wb=wb: ops.linear(x, wb) for wb in wbs], a.iters, a.warmup)
@@ -210,7 +211,7 @@ def main(argv: list[str] | None = None) -> None:
     p.add_argument("--m", type=int, default=61)
     p.add_argument("--n", type=int, default=6144)
     p.add_argument("--k", type=int, default=4096)
-    p.add_argument("--fmt", default="int4", choices=["int4", "int8", "fp8"])
+    p.add_argument("--fmt", default="int4", choices=["int2", "int4", "int8", "fp8", "mxfp4", "nvfp4"])
     p.add_argument("--group", type=int, default=128)
     p.add_argument("--batch", type=int, default=1)
     p.add_argument("--tree", type=int, default=61)

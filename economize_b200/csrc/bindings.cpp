@@ -342,18 +342,26 @@ Tensor linear_wq(Tensor x, Tensor qweight, Tensor scales, c10::optional<Tensor> 
   CHECK_BF16(x);
   CHECK_BF16(scales);
   TORCH_CHECK(qweight.scalar_type() == at::kByte, "qweight must be uint8");
-  TORCH_CHECK(fmt == ecz::kWqInt4 || fmt == ecz::kWqInt8 || fmt == ecz::kWqFp8 || fmt == ecz::kWqInt2,
+  TORCH_CHECK(fmt == ecz::kWqInt4 || fmt == ecz::kWqInt8 || fmt == ecz::kWqFp8 || fmt == ecz::kWqInt2 ||
+                  fmt == ecz::kWqMxfp4 || fmt == ecz::kWqNvfp4,
               "unknown weight format ", fmt);
+  const bool fp4 = fmt == ecz::kWqMxfp4 || fmt == ecz::kWqNvfp4;
   const bool zp = fmt == ecz::kWqInt4 || fmt == ecz::kWqInt2;
   TORCH_CHECK(x.dim() == 2 && qweight.dim() == 2 && scales.dim() == 2, "linear_wq expects 2-D operands");
   c10::cuda::CUDAGuard guard(x.device());
   x = x.contiguous();
   TORCH_CHECK(qweight.is_contiguous() && scales.is_contiguous(), "packed weights and scales must be contiguous");
   const int M = static_cast<int>(x.size(0)), K = static_cast<int>(x.size(1)), N = static_cast<int>(qweight.size(0));
-  const int row_bytes = fmt == ecz::kWqInt4 ? K / 2 : fmt == ecz::kWqInt2 ? K / 4 : K;
+  const int row_bytes = fmt == ecz::kWqInt4 || fp4 ? K / 2 : fmt == ecz::kWqInt2 ? K / 4 : K;
   TORCH_CHECK(qweight.size(1) == row_bytes, "qweight has ", qweight.size(1), " bytes per row, expected ", row_bytes);
   TORCH_CHECK(K % group == 0 && scales.size(0) == K / group && scales.size(1) == N, "scales must be [K / group, N]");
-  TORCH_CHECK(K % 64 == 0 && group % 64 == 0 && N % 8 == 0, "linear_wq: K and group must be multiples of 64, N of 8");
+  if (fp4) {
+    TORCH_CHECK(group == (fmt == ecz::kWqMxfp4 ? 32 : 16), "mxfp4 takes group 32, nvfp4 group 16");
+    TORCH_CHECK(K % 64 == 0 && N % 8 == 0, "linear_wq: K must be a multiple of 64, N of 8");
+  } else {
+    TORCH_CHECK(K % 64 == 0 && group % 64 == 0 && N % 8 == 0,
+                "linear_wq: K and group must be multiples of 64, N of 8");
+  }
   Tensor z;
   if (zp) {
     TORCH_CHECK(zeros.has_value(), "int4 / int2 weights need zeros");
@@ -366,8 +374,9 @@ Tensor linear_wq(Tensor x, Tensor qweight, Tensor scales, c10::optional<Tensor> 
   const int bn = ecz::gemm_block_n(M);
   ecz::WqMaps maps;
   maps.w = tensor_map_ex(qweight.data_ptr(), 1, N, row_bytes, row_bytes,
-                         fmt == ecz::kWqInt4 ? 32 : fmt == ecz::kWqInt2 ? 16 : 64, 128, 0);
-  maps.s = tensor_map_ex(scales.data_ptr(), 2, K / group, N, static_cast<uint64_t>(N) * 2, 128, 1, 0);
+                         fmt == ecz::kWqInt4 || fp4 ? 32 : fmt == ecz::kWqInt2 ? 16 : 64, 128, 0);
+  maps.s = tensor_map_ex(scales.data_ptr(), 2, K / group, N, static_cast<uint64_t>(N) * 2, 128,
+                         fp4 ? 64 / static_cast<int>(group) : 1, 0);
   if (zp) maps.z = tensor_map_ex(z.data_ptr(), 2, K / group, N, static_cast<uint64_t>(N) * 2, 128, 1, 0);
   maps.x = tensor_map(x.data_ptr(), M, K, K, bn);
   const int sp = splits > 0 ? static_cast<int>(splits)

@@ -23,9 +23,15 @@
 //         (per row and 64-wide K-block 8 bytes, 4 bits per group of 4: the two kept positions; rows 2p and 2p + 1
 //         share a 16-byte line). The expansion to dense bf16 happens in shared memory, so a decode pass streams 56 %
 //         of the dense bytes.
+//   mxfp4 / nvfp4  uint8 [N, K/2] FP4 E2M1 codes, k = 2b in the low and 2b + 1 in the high nibble of byte b; the
+//         scale group is 32 K (MX) or 16 K (NV), so a stage carries 2 or 4 scale rows and each 8-K chunk picks its
+//         group's scale. The stored bf16 scale is the effective one (MX: the E8M0 power of two; NV: the e4m3 group
+//         scale times the power-of-two inverse global scale), exact in bf16. (economize's fp4 grids,
+//         src/economize/techniques/quant/fp4.py:1-60; Blackwell W4A16: the codes stream at 4.25 / 4.5 bits.)
 // scales bf16 [K/group, N]; zeros (int4) bf16 [K/group, N] holding 128 + z, so that (128 + q) - (128 + z) = q - z.
 #include <algorithm>
 
+#include <cuda_fp4.h>
 #include <cuda_fp8.h>
 
 #include "common.cuh"
@@ -43,12 +49,15 @@ constexpr int kThreads = 192;
 
 template <int FMT>
 struct WqFmt {
-  // int4: 32 B of codes per row and K-block; int8/fp8: 64 B; 2:4 sparse: the 32 kept bf16 values (64 B)
-  static constexpr int kRawRowBytes = FMT == kWqInt4 ? kBK / 2 : FMT == kWqInt2 ? kBK / 4 : kBK;
+  static constexpr bool kFp4 = FMT == kWqMxfp4 || FMT == kWqNvfp4;
+  // int4 / fp4: 32 B of codes per row and K-block; int8/fp8: 64 B; 2:4 sparse: the 32 kept bf16 values (64 B)
+  static constexpr int kRawRowBytes = FMT == kWqInt4 || kFp4 ? kBK / 2 : FMT == kWqInt2 ? kBK / 4 : kBK;
   static constexpr int kRawBytes = kBM * kRawRowBytes;
   static constexpr bool kZeros = FMT == kWqInt4 || FMT == kWqInt2;
-  // per-stage side data: one bf16 scale per row, or the 2:4 positions (8 B per row)
-  static constexpr int kSideBytes = FMT == kWqSp24 ? kBM * 8 : kBM * 2;
+  // scale rows per K-block: fp4 formats have a scale per 32 (MX) or 16 (NV) K, the others one per >= 64 K
+  static constexpr int kScaleRows = FMT == kWqMxfp4 ? kBK / 32 : FMT == kWqNvfp4 ? kBK / 16 : 1;
+  // per-stage side data: bf16 scales [kScaleRows][128 rows], or the 2:4 positions (8 B per row)
+  static constexpr int kSideBytes = FMT == kWqSp24 ? kBM * 8 : kBM * 2 * kScaleRows;
 };
 
 template <int FMT, int BN>
@@ -109,6 +118,15 @@ __device__ __forceinline__ uint4 dequant_chunk(const uint32_t* w, int j, __nv_bf
         const __nv_bfloat162 q = __hfma2(hi, c16, lo);                       // exact: |q| <= 128
         out[2 * h + p] = bf2_bits(__hmul2(q, s2));
       }
+    }
+  } else if constexpr (FMT == kWqMxfp4 || FMT == kWqNvfp4) {
+    // byte i of word j holds k = 8j + 2i (low nibble) and 8j + 2i + 1 (high nibble) as FP4 E2M1 codes
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const __nv_fp4x2_storage_t pair = static_cast<__nv_fp4x2_storage_t>((w[j] >> (8 * i)) & 0xFFu);
+      const __half2 hv = __half2(__nv_cvt_fp4x2_to_halfraw2(pair, __NV_E2M1));
+      const __nv_bfloat162 b = __float22bfloat162_rn(__half22float2(hv));  // exact: E2M1 values fit bf16
+      out[i] = bf2_bits(__hmul2(b, s2));
     }
   } else {
 #pragma unroll
@@ -215,7 +233,9 @@ __global__ void __launch_bounds__(kThreads, WqCfg<FMT, BN>::kOcc)
         return;
       }
       tma_load_2d(raw + s * F::kRawBytes, &tm_w, &full[s], k * F::kRawRowBytes / kBK, n0);
-      tma_load_2d(scales + s * kBM, &tm_s, &full[s], n0, k / group);
+      // fp4: the kScaleRows scale rows of this K-block (group = kBK / kScaleRows); else the one row k / group
+      tma_load_2d(reinterpret_cast<uint8_t*>(scales) + s * F::kSideBytes, &tm_s, &full[s], n0,
+                  F::kScaleRows > 1 ? k / kBK * F::kScaleRows : k / group);
       if (F::kZeros) tma_load_2d(zeros + s * kBM, &tm_z, &full[s], n0, k / group);
     };
     for (int kb = 0; kb < pre; ++kb) {
@@ -262,7 +282,7 @@ __global__ void __launch_bounds__(kThreads, WqCfg<FMT, BN>::kOcc)
       if constexpr (FMT == kWqSp24) {
         meta = *reinterpret_cast<const uint64_t*>(reinterpret_cast<const uint8_t*>(scales) + s * F::kSideBytes +
                                                   (row >> 1) * 16 + (row & 1) * 8);
-      } else {
+      } else if constexpr (F::kScaleRows == 1) {
         sc = scales[s * kBM + row];
       }
       const __nv_bfloat162 s2 = __halves2bfloat162(sc, sc);
@@ -282,8 +302,14 @@ __global__ void __launch_bounds__(kThreads, WqCfg<FMT, BN>::kOcc)
 #pragma unroll
       for (int j = 0; j < 8; ++j) {
         uint4 v;
-        if constexpr (FMT == kWqSp24) v = expand_sp24(words, meta, j);
-        else v = dequant_chunk<FMT>(words, j, s2, z2);
+        if constexpr (FMT == kWqSp24) {
+          v = expand_sp24(words, meta, j);
+        } else if constexpr (F::kScaleRows > 1) {  // fp4: the scale of the group holding k = 8j .. 8j + 7
+          const bf16 sj = scales[s * (F::kSideBytes / 2) + (j * F::kScaleRows / 8) * kBM + row];
+          v = dequant_chunk<FMT>(words, j, __halves2bfloat162(sj, sj), z2);
+        } else {
+          v = dequant_chunk<FMT>(words, j, s2, z2);
+        }
         *reinterpret_cast<uint4*>(dst_row + ((j ^ (row & 7)) << 4)) = v;
       }
       fence_async_smem();
@@ -407,7 +433,7 @@ int gemm_wq_splits(int M, int N, int K, int fmt, int num_sms) {
   const int tiles = ((N + kBM - 1) / kBM) * ((M + gemm_block_n(M) - 1) / gemm_block_n(M));
   const int kb = K / kBK;
   // at least 8 K-blocks (512 K) per CTA for int8/fp8, 16 for int4: below that the prologue dominates
-  const int min_kb = fmt == kWqInt2 ? 32 : fmt == kWqInt4 ? 16 : 8;
+  const int min_kb = fmt == kWqInt2 ? 32 : (fmt == kWqInt4 || fmt == kWqMxfp4 || fmt == kWqNvfp4) ? 16 : 8;
   int splits = std::max(1, std::min(slots / std::max(1, tiles), kb / min_kb));
   return std::min(8, splits);
 }
@@ -415,13 +441,17 @@ int gemm_wq_splits(int M, int N, int K, int fmt, int num_sms) {
 int launch_gemm_wq(const WqMaps& maps, void* y, int M, int N, int K, int group, int fmt, int splits,
                    unsigned* status, cudaStream_t stream) {
   if (M <= 0 || N <= 0) return 0;
-  if (K % kBK != 0 || group % kBK != 0 || K % group != 0 || N % 8 != 0 || splits < 1 || splits > 8) return -1;
+  const int fp4_group = fmt == kWqMxfp4 ? 32 : fmt == kWqNvfp4 ? 16 : 0;
+  if (fp4_group ? group != fp4_group : group % kBK != 0) return -1;
+  if (K % kBK != 0 || K % group != 0 || N % 8 != 0 || splits < 1 || splits > 8) return -1;
   switch (fmt) {
     case kWqInt4: return run_wq_bn<kWqInt4>(maps, y, M, N, K, group, splits, status, stream);
     case kWqInt8: return run_wq_bn<kWqInt8>(maps, y, M, N, K, group, splits, status, stream);
     case kWqFp8: return run_wq_bn<kWqFp8>(maps, y, M, N, K, group, splits, status, stream);
     case kWqSp24: return run_wq_bn<kWqSp24>(maps, y, M, N, K, K, splits, status, stream);
     case kWqInt2: return run_wq_bn<kWqInt2>(maps, y, M, N, K, group, splits, status, stream);
+    case kWqMxfp4: return run_wq_bn<kWqMxfp4>(maps, y, M, N, K, group, splits, status, stream);
+    case kWqNvfp4: return run_wq_bn<kWqNvfp4>(maps, y, M, N, K, group, splits, status, stream);
     default: return -1;
   }
 }

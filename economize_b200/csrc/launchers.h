@@ -110,7 +110,7 @@ int launch_reduce_rmsnorm(const PeerPtrs& peers, int rank, int world, int parity
                           unsigned* status, cudaStream_t stream);
 
 // gemm_wq.cu: weight-only quantized GEMM (W4A16 / W8A16 / fp8-weight); see the file comment for the layouts.
-enum WqFormat : int { kWqInt4 = 0, kWqInt8 = 1, kWqFp8 = 2, kWqSp24 = 3, kWqInt2 = 4 };
+enum WqFormat : int { kWqInt4 = 0, kWqInt8 = 1, kWqFp8 = 2, kWqSp24 = 3, kWqInt2 = 4, kWqMxfp4 = 5, kWqNvfp4 = 6 };
 struct WqMaps {
   const CUtensorMap* w = nullptr;  // packed weights, uint8 [N, K * bits / 8], box {64 * bits / 8, 128}
   const CUtensorMap* s = nullptr;  // scales bf16 [K / group, N], box {128, 1}

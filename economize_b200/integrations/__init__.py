@@ -1,0 +1,2 @@
+"""Integrations with other tools' file formats (economize ``src/economize/integrations``):
+:mod:`~economize_b200.integrations.compressed_tensors` writes quantized targets for llm-compressor's loaders."""

@@ -16,6 +16,10 @@ Formats (economize's ``QUANT_FORMATS`` names, ``src/economize/techniques/quant/g
 * ``int3``: codes 0..7 with zero points, stored in the ``int4`` layout (the kernel's int4 path dequantizes them).
 * ``int2``: codes 0..3 with zero points, 16 per 32-bit word (bits ``2m`` of the low half hold ``k_2m``, of the high
   half ``k_2m+1``), so the kernel extracts a bf16 pair with one shift and one mask as for int4.
+* ``mxfp4`` / ``nvfp4``: FP4 E2M1 codes (bits 0-2 index :data:`E2M1_VALUES`, bit 3 the sign), two per byte with
+  ``k = 2b`` in the low nibble of byte ``b``; one scale per 32 (MX) or 16 (NV) input columns. The stored bf16 scale
+  is the effective one: MX's E8M0 power of two, or NV's e4m3 group scale divided by the tensor's global scale
+  (chosen as a power of two here, so the quotient stays exact in bf16).
 
 Scales (and zeros) are ``[K / group, N]`` bf16: one 256-byte row per 128 output features and group, which the kernel
 reads with one TMA box. The dequantized weight is ``bf16((q - z) * s)`` in every path (the kernel's bf16x2
@@ -29,12 +33,40 @@ from torch import nn
 
 from ..errors import ConfigError
 
-__all__ = ["FORMAT_CODES", "ZERO_POINT_FORMATS", "QWeight", "dequantize", "install", "pack", "unpack"]
+__all__ = ["CODES_PER_BYTE", "E2M1_VALUES", "FORMAT_CODES", "FP4_GROUP", "ZERO_POINT_FORMATS", "QWeight", "dequantize",
+           "e2m1_round", "install", "pack", "unpack"]
 
 #: kernel format codes (``WqFormat`` in ``csrc/launchers.h``); int3 codes (0..7) are stored in the int4 layout
-FORMAT_CODES = {"int4": 0, "int8": 1, "fp8": 2, "int3": 0, "int2": 4}
+FORMAT_CODES = {"int4": 0, "int8": 1, "fp8": 2, "int3": 0, "int2": 4, "mxfp4": 5, "nvfp4": 6}
 #: formats with a zero point per (row, group) (the bf16 value ``128 + z``)
 ZERO_POINT_FORMATS = ("int2", "int3", "int4")
+#: codes per stored byte (1 for the 8-bit formats)
+CODES_PER_BYTE = {"int4": 2, "int3": 2, "int2": 4, "mxfp4": 2, "nvfp4": 2}
+#: the fixed scale group of the FP4 formats
+FP4_GROUP = {"mxfp4": 32, "nvfp4": 16}
+#: the non-negative FP4 E2M1 values, indexed by the low three bits of a code
+E2M1_VALUES = (0.0, 0.5, 1.0, 1.5, 2.0, 3.0, 4.0, 6.0)
+
+
+def e2m1_round(x: torch.Tensor) -> torch.Tensor:
+    """``x`` rounded to the nearest E2M1 value (magnitudes above 6 clip to 6; a tie goes to the value with the even
+    code, IEEE round-half-to-even on the 3-bit magnitude index)."""
+    table = torch.tensor(E2M1_VALUES, dtype=torch.float32, device=x.device)
+    a = x.float().abs().clamp(max=6.0)
+    hi = torch.bucketize(a, table)  # table[hi - 1] < a <= table[hi]
+    lo = (hi - 1).clamp(min=0)
+    d_lo, d_hi = a - table[lo], table[hi] - a
+    pick = torch.where((d_hi < d_lo) | ((d_hi == d_lo) & (hi % 2 == 0)), hi, lo)
+    return torch.copysign(table[pick], x.float()) * (pick > 0)
+
+
+def _fp4_codes(values: torch.Tensor) -> torch.Tensor:
+    """E2M1 values -> 4-bit codes (int64); zero is code 0 whatever its sign."""
+    twice = (values.float().abs() * 2).round().to(torch.int64)  # 0, 1, 2, 3, 4, 6, 8, 12
+    index = torch.tensor([0, 1, 2, 3, 4, -1, 5, -1, 6, -1, -1, -1, 7], device=values.device)[twice.clamp(max=12)]
+    if (index < 0).any() or (values.float().abs() > 6).any():
+        raise ConfigError("fp4 packing takes E2M1 values (0, 0.5, 1, 1.5, 2, 3, 4, 6 and their negatives)")
+    return index | ((values < 0) & (index > 0)).to(torch.int64) << 3
 _INT4_ORDER = (0, 2, 4, 6, 1, 3, 5, 7)
 _INT8_ORDER = (0, 2, 1, 3)
 
@@ -71,11 +103,14 @@ def pack(codes: torch.Tensor, fmt: str) -> torch.Tensor:
         return u.to(torch.uint8).reshape(n, k)
     if fmt == "fp8":
         return codes.to(torch.float8_e4m3fn).contiguous().view(torch.uint8)
+    if fmt in FP4_GROUP:  # E2M1 values; k = 2b in the low nibble of byte b
+        c = _fp4_codes(codes).reshape(n, k // 2, 2)
+        return (c[..., 0] | (c[..., 1] << 4)).to(torch.uint8)
     raise ConfigError(f"unknown weight format {fmt!r}")
 
 
 def unpack(data: torch.Tensor, fmt: str) -> torch.Tensor:
-    """Inverse of :func:`pack`: int64 codes (int4, int8) or fp32 values (fp8) ``[N, K]``."""
+    """Inverse of :func:`pack`: int64 codes (int2, int4, int8) or fp32 values (fp8, fp4) ``[N, K]``."""
     n = data.shape[0]
     if fmt == "int2":
         words = _bytes_to_words(data)
@@ -97,6 +132,11 @@ def unpack(data: torch.Tensor, fmt: str) -> torch.Tensor:
         return out.reshape(n, -1) - 128
     if fmt == "fp8":
         return data.contiguous().view(torch.float8_e4m3fn).float()
+    if fmt in FP4_GROUP:
+        b = data.to(torch.int64)
+        codes = torch.stack([b & 0xF, b >> 4], -1).reshape(n, -1)
+        table = torch.tensor(E2M1_VALUES, dtype=torch.float32, device=data.device)
+        return torch.where(codes >= 8, -table[codes & 7], table[codes & 7])
     raise ConfigError(f"unknown weight format {fmt!r}")
 
 
@@ -117,7 +157,7 @@ class QWeight(nn.Module):
         qweight: Packed codes (:func:`pack`).
         scales: ``[K / group, N]`` bf16.
         zeros: ``[K / group, N]`` bf16 holding ``128 + z`` (int4), else ``None``.
-        fmt: ``"int2"``, ``"int3"``, ``"int4"``, ``"int8"`` or ``"fp8"``.
+        fmt: ``"int2"``, ``"int3"``, ``"int4"``, ``"int8"``, ``"fp8"``, ``"mxfp4"`` or ``"nvfp4"``.
         group: Input columns per scale (``in_features`` for one scale per output row).
         dtype: The activation dtype the layer computes in.
     """
@@ -130,7 +170,7 @@ class QWeight(nn.Module):
         self.fmt = fmt
         self.group = int(group)
         self.out_features = int(qweight.shape[0])
-        self.in_features = int(qweight.shape[1] * {"int4": 2, "int3": 2, "int2": 4}.get(fmt, 1))
+        self.in_features = int(qweight.shape[1] * CODES_PER_BYTE.get(fmt, 1))
         self.compute_dtype = dtype
         self.register_buffer("qweight", qweight.contiguous())
         self.register_buffer("scales", scales.to(torch.bfloat16).contiguous())
@@ -150,7 +190,7 @@ class QWeight(nn.Module):
 
     @property
     def bits(self) -> int:
-        return {"int2": 2, "int3": 3, "int4": 4}.get(self.fmt, 8)
+        return {"int2": 2, "int3": 3, "int4": 4, "mxfp4": 4, "nvfp4": 4}.get(self.fmt, 8)
 
     def dequantize(self, dtype: torch.dtype | None = None) -> torch.Tensor:
         return dequantize(self.qweight, self.scales, self.zeros, self.fmt, self.group, dtype or self.compute_dtype)
@@ -180,7 +220,7 @@ class QWeight(nn.Module):
         """The input columns ``[start, stop)`` (a row-parallel shard); both ends must sit on group boundaries."""
         if start % self.group or stop % self.group:
             raise ConfigError(f"column shard [{start}, {stop}) cuts a quantization group of {self.group}")
-        per = {"int4": 2, "int3": 2, "int2": 4}.get(self.fmt, 1)
+        per = CODES_PER_BYTE.get(self.fmt, 1)
         z = None if self.zeros is None else self.zeros[start // self.group: stop // self.group]
         return QWeight(self.qweight[:, start // per: stop // per], self.scales[start // self.group: stop // self.group],
                        z, self.fmt, self.group, self.compute_dtype)

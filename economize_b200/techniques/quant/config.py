@@ -17,8 +17,8 @@ from ...validation import check_choice, check_positive
 
 __all__ = ["DraftQuantConfig", "QUANT_FORMATS", "QUANT_METHODS_NAMES", "QuantConfig"]
 
-#: formats the packed kernel layout stores (economize also simulates int2/int3 and fp4 grids)
-QUANT_FORMATS = ("int2", "int3", "int4", "int8", "fp8", "fp8_block")
+#: formats the packed kernel layout stores
+QUANT_FORMATS = ("int2", "int3", "int4", "int8", "fp8", "fp8_block", "mxfp4", "nvfp4")
 QUANT_METHODS_NAMES = ("rtn", "gptq", "awq", "hqq", "smoothquant")
 #: engine projection names and the Hugging Face module names fused into them
 PROJECTIONS = {"wqkv": ("self_attn.q_proj", "self_attn.k_proj", "self_attn.v_proj"), "wo": ("self_attn.o_proj",),
@@ -44,7 +44,8 @@ class QuantConfig(TechniqueConfig):
 
     Args:
         format: ``"int4"`` (default, GPTQ/AWQ W4A16), ``"int3"`` / ``"int2"`` (W3A16 in the int4 layout, W2A16
-            packed 16 per word), ``"int8"`` (W8A16), ``"fp8"`` (e4m3 weights, bf16
+            packed 16 per word), ``"mxfp4"`` / ``"nvfp4"`` (FP4 E2M1 weights with a scale per 32 / 16 columns;
+            ``group_size`` and ``symmetric`` do not apply), ``"int8"`` (W8A16), ``"fp8"`` (e4m3 weights, bf16
             activations) or ``"fp8_block"`` (W8A8: e4m3 weights with 128 x 128 block scales and activations
             quantised per token and 128-wide block on the fly; ``group_size`` is ignored).
         method: ``"rtn"`` (round to nearest, no data), ``"hqq"`` (half-quadratic fit of the grid, no data),
@@ -99,6 +100,8 @@ class QuantConfig(TechniqueConfig):
             raise ConfigError("layers are 1-indexed")
         if self.method in ("gptq", "awq", "hqq") and self.format in ("fp8", "fp8_block"):
             raise ConfigError(f"{self.method} fits integer grids; use method='rtn' for fp8")
+        if self.method in ("hqq", "smoothquant") and self.format in ("mxfp4", "nvfp4"):
+            raise ConfigError(f"{self.method} does not fit FP4 grids; use rtn, gptq or awq")
         check_positive("hqq_iters", self.hqq_iters)
         if not 0.0 < self.hqq_p <= 1.0 or not 0.0 <= self.smooth_alpha <= 1.0:
             raise ConfigError("hqq_p must lie in (0, 1] and smooth_alpha in [0, 1]")

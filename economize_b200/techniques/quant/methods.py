@@ -24,7 +24,7 @@ from collections.abc import Callable, Sequence
 import torch
 
 from ...errors import ConfigError
-from ...ops.quant import QWeight, pack
+from ...ops.quant import FP4_GROUP, QWeight, e2m1_round, pack
 
 __all__ = ["Grid", "awq_search", "collect", "fit_grid", "gptq", "quantize_codes", "rtn"]
 
@@ -44,8 +44,37 @@ class Grid:
         self.scale, self.zero = scale, zero
 
 
-def fit_grid(w: torch.Tensor, fmt: str, symmetric: bool, clip: torch.Tensor | float = 1.0) -> Grid:
-    """Grid of ``w [N, G, g]`` (groups along the last axis); ``clip`` shrinks the range (AWQ's clipping)."""
+def _mx_scale(amax: torch.Tensor) -> torch.Tensor:
+    """MXFP4 group scale: ``2^(e - 2)`` with ``e`` the exponent of ``amax`` rounded to a power of two (up when its
+    mantissa is at least 1.75, so the group maximum lands at 4..7 units instead of clipping at 6)."""
+    e = torch.floor(torch.log2(amax.clamp(min=2.0 ** -120)))
+    e = torch.where(amax / torch.exp2(e) >= 1.75, e + 1, e)
+    return torch.where(amax > 0, torch.exp2(e - 2), torch.ones_like(amax))
+
+
+def nvfp4_global_scale(amax: float) -> float:
+    """NVFP4 global scale: the power of two at or below ``448 * 6 / amax`` (so the largest group scale fits e4m3 and
+    every effective scale ``s8 / global`` is exact in bf16)."""
+    if amax <= 0:
+        return 1.0
+    return float(2.0 ** math.floor(math.log2(448.0 * 6.0 / amax)))
+
+
+def _fp4_grid(w: torch.Tensor, fmt: str, clip, tensor_amax: float | None) -> Grid:
+    amax = w.abs().amax(-1) * clip
+    if fmt == "mxfp4":
+        return Grid(_mx_scale(amax), None)
+    glob = nvfp4_global_scale(float(w.abs().max()) if tensor_amax is None else float(tensor_amax))
+    s8 = (amax / 6.0 * glob).clamp(2.0 ** -9, 448.0).to(torch.float8_e4m3fn).float()
+    return Grid(s8.clamp(min=2.0 ** -9) / glob, None)
+
+
+def fit_grid(w: torch.Tensor, fmt: str, symmetric: bool, clip: torch.Tensor | float = 1.0,
+             tensor_amax: float | None = None) -> Grid:
+    """Grid of ``w [N, G, g]`` (groups along the last axis); ``clip`` shrinks the range (AWQ's clipping).
+    ``tensor_amax``: the whole weight's absolute maximum, for NVFP4's global scale when ``w`` is part of it."""
+    if fmt in FP4_GROUP:
+        return _fp4_grid(w, fmt, clip, tensor_amax)
     top = _INT_TOP.get(fmt)
     if top is not None and not symmetric:
         hi = (w.amax(-1) * clip).clamp(min=0)
@@ -72,6 +101,9 @@ def quantize_codes(w: torch.Tensor, grid: Grid, fmt: str) -> tuple[torch.Tensor,
     if fmt == "int8":
         q = torch.clamp(torch.round(w / s), -128, 127)
         return q, (q * s).to(torch.bfloat16).float()
+    if fmt in FP4_GROUP:
+        q = e2m1_round(w / s)
+        return q, (q * s).to(torch.bfloat16).float()
     q = (w / s).clamp(-FP8_MAX, FP8_MAX).to(torch.float8_e4m3fn).float()
     return q, (q * s).to(torch.bfloat16).float()
 
@@ -79,7 +111,8 @@ def quantize_codes(w: torch.Tensor, grid: Grid, fmt: str) -> tuple[torch.Tensor,
 def _qweight(codes: torch.Tensor, grid: Grid, fmt: str, group: int, dtype: torch.dtype) -> QWeight:
     n = codes.shape[0]
     codes = codes.reshape(n, -1)
-    packed = pack(codes.to(torch.float8_e4m3fn) if fmt == "fp8" else codes.to(torch.int64), fmt)
+    packed = pack(codes.to(torch.float8_e4m3fn) if fmt == "fp8" else codes if fmt in FP4_GROUP
+                  else codes.to(torch.int64), fmt)
     scales = grid.scale.t().contiguous().to(torch.bfloat16)
     zeros = (grid.zero.t() + 128.0).contiguous().to(torch.bfloat16) if fmt in _INT_TOP else None
     return QWeight(packed, scales, zeros, fmt, group, dtype)
@@ -94,8 +127,8 @@ def _groups(w: torch.Tensor, group: int) -> torch.Tensor:
 
 def rtn(weight: torch.Tensor, fmt: str, group: int | None, symmetric: bool,
         clip: torch.Tensor | float = 1.0) -> QWeight:
-    """Round-to-nearest quantization of ``weight [N, K]``."""
-    g = group or weight.shape[1]
+    """Round-to-nearest quantization of ``weight [N, K]`` (FP4 formats use their own group of 32 or 16)."""
+    g = FP4_GROUP.get(fmt) or group or weight.shape[1]
     w = _groups(weight.float(), g)
     grid = fit_grid(w, fmt, symmetric, clip)
     codes, _ = quantize_codes(w, grid, fmt)
@@ -108,14 +141,15 @@ def gptq(weight: torch.Tensor, hessian: torch.Tensor, fmt: str, group: int | Non
     """GPTQ of ``weight [N, K]`` given ``hessian [K, K]`` (``X^T X`` summed over calibration rows)."""
     W = weight.float().clone()
     n, k = W.shape
-    g = group or k
+    g = FP4_GROUP.get(fmt) or group or k
+    tensor_amax = float(W.abs().max())
     H = hessian.float().clone()
     dead = torch.diag(H) == 0
     H[dead, dead] = 1.0
     W[:, dead] = 0.0
     static = None
     if act_order:  # fit every group on the original contiguous columns, then visit columns by saliency
-        static = fit_grid(_groups(W, g), fmt, symmetric)
+        static = fit_grid(_groups(W, g), fmt, symmetric, tensor_amax=tensor_amax)
         perm = torch.argsort(torch.diag(H), descending=True)
         W, H = W[:, perm], H[perm][:, perm]
         inv_perm = torch.argsort(perm)
@@ -140,7 +174,7 @@ def gptq(weight: torch.Tensor, hessian: torch.Tensor, fmt: str, group: int | Non
                 cur = Grid(static.scale[:, grp:grp + 1], None if static.zero is None else static.zero[:, grp:grp + 1])
             elif col % g == 0:
                 span = W1[:, i:i + g] if i + g <= i2 - i1 else torch.cat([W1[:, i:], W[:, i2:col + g]], 1)
-                cur = fit_grid(span[:, None, :], fmt, symmetric)
+                cur = fit_grid(span[:, None, :], fmt, symmetric, tensor_amax=tensor_amax)
                 scale[:, grp] = cur.scale[:, 0]
                 if zero is not None:
                     zero[:, grp] = cur.zero[:, 0]
@@ -227,6 +261,7 @@ def collect(model, batches: Sequence[torch.Tensor], wanted: dict[int, Sequence[s
 # ---- AWQ -----------------------------------------------------------------------------------------------------
 def _awq_loss(x: torch.Tensor, w: torch.Tensor, s: torch.Tensor, fmt: str, group: int, symmetric: bool) -> float:
     """Output error of quantizing ``w * s`` and feeding ``x / s``."""
+    group = FP4_GROUP.get(fmt, group)
     ws = w * s[None, :]
     wq = _groups(ws, group)
     grid = fit_grid(wq, fmt, symmetric)
@@ -258,6 +293,7 @@ def awq_search(weights: Sequence[torch.Tensor], stats: _Stats, fmt: str, group: 
 def awq_clip(weight: torch.Tensor, x: torch.Tensor, fmt: str, group: int, symmetric: bool,
              grid_points: int, max_shrink: float = 0.5) -> torch.Tensor:
     """Per (row, group) clipping ratio minimising the group's output error on the sample ``x``."""
+    group = FP4_GROUP.get(fmt, group)
     w = _groups(weight.float(), group)  # [N, G, g]
     xg = x.float().reshape(x.shape[0], -1, group)  # [T, G, g]
     ref = torch.einsum("ngk,tgk->ngt", w, xg)

@@ -16,7 +16,7 @@ from torch import nn
 from ...core.technique import Capability, Family, Technique, register_technique
 from ...errors import ConfigError
 from ...ops.fp8 import FP8BlockWeight
-from ...ops.quant import QWeight, install
+from ...ops.quant import CODES_PER_BYTE, FP4_GROUP, QWeight, install
 from . import methods
 from .config import PROJECTIONS, DraftQuantConfig, QuantConfig
 
@@ -70,8 +70,8 @@ class _QuantBase(Technique):
             if "codes" in bufs:
                 self.weights[key] = FP8BlockWeight(bufs["codes"], bufs["scales"], self._dtype())
                 continue
-            k_in = bufs["qweight"].shape[1] * {"int4": 2, "int3": 2, "int2": 4}.get(cfg.format, 1)
-            group = cfg.group_size or k_in
+            k_in = bufs["qweight"].shape[1] * CODES_PER_BYTE.get(cfg.format, 1)
+            group = FP4_GROUP.get(cfg.format) or cfg.group_size or k_in
             self.weights[key] = QWeight(bufs["qweight"], bufs["scales"], bufs.get("zeros"), cfg.format, group,
                                         self._dtype())
 

@@ -133,7 +133,7 @@ def test_config_checks():
 
 # ---- GPU ------------------------------------------------------------------------------------------------------
 @pytest.mark.gpu
-@pytest.mark.parametrize("fmt", ["int2", "int3", "int4", "int8", "fp8"])
+@pytest.mark.parametrize("fmt", ["int2", "int3", "int4", "int8", "fp8", "mxfp4", "nvfp4"])
 @pytest.mark.parametrize("M,N,K,group", [(1, 4096, 4096, 128), (61, 6144, 4096, 128), (7, 264, 512, 64),
                                          (200, 1024, 2048, 2048), (600, 512, 1024, 128)])
 def test_linear_wq_matches_fp32(cuda, fmt, M, N, K, group):
@@ -253,3 +253,64 @@ def test_smoothquant_fp8_block_decodes_and_moves_outliers():
     em = eco.apply(tiny_model(), QuantConfig(format="fp8_block", method="smoothquant", group_size=None),
                    calibration=cal)
     assert em.decode(prompts((10,))[0], 4).tokens.numel() == 4
+
+
+# ---- FP4 (MXFP4 / NVFP4) ------------------------------------------------------------------------------------------
+def test_e2m1_rounding_ties_and_clipping():
+    from economize_b200.ops.quant import e2m1_round
+
+    x = torch.tensor([0.25, 0.75, 1.25, 1.75, 2.5, 3.5, 5.0, 0.3, 2.6, 7.0, -9.0, -0.2, -1.3])
+    assert e2m1_round(x).tolist() == [0.0, 1.0, 1.0, 2.0, 2.0, 4.0, 4.0, 0.5, 3.0, 6.0, -6.0, 0.0, -1.5]
+
+
+@pytest.mark.parametrize("fmt", ["mxfp4", "nvfp4"])
+def test_fp4_pack_roundtrip_and_layout(fmt):
+    from economize_b200.ops.quant import E2M1_VALUES
+
+    g = torch.Generator().manual_seed(0)
+    vals = torch.tensor(E2M1_VALUES)[torch.randint(0, 8, (16, 64), generator=g)]
+    vals = vals * torch.where(torch.rand(16, 64, generator=g) < 0.5, -1.0, 1.0)
+    packed = pack(vals, fmt)
+    assert packed.shape == (16, 32) and torch.equal(unpack(packed, fmt), vals + 0.0)  # -0 reads back as 0
+    one = torch.zeros(1, 64)
+    one[0, 0], one[0, 1] = 1.5, -6.0  # codes 3 and 8 | 7
+    assert pack(one, fmt)[0, 0].item() == 0x3 | (0xF << 4)
+
+
+@pytest.mark.parametrize("fmt,group,tol", [("mxfp4", 32, 0.16), ("nvfp4", 16, 0.13)])
+def test_fp4_rtn(fmt, group, tol):
+    from economize_b200.techniques.quant.methods import fit_grid
+
+    g = torch.Generator().manual_seed(1)
+    w = torch.randn(64, 256, generator=g) * 0.02
+    qw = rtn(w, fmt, 128, False)
+    assert qw.group == group and qw.scales.shape == (256 // group, 64) and qw.bits == 4
+    err = (qw.dequantize(torch.float32) - w).norm() / w.norm()
+    assert err < tol
+    grid = fit_grid(w.reshape(64, -1, group), fmt, True)
+    assert torch.equal(grid.scale.to(torch.bfloat16).float(), grid.scale)  # effective scales exact in bf16
+    if fmt == "mxfp4":  # powers of two
+        assert torch.equal(torch.exp2(torch.log2(grid.scale).round()), grid.scale)
+    units = w.reshape(64, -1, group).abs().amax(-1) / grid.scale  # the group maximum in scale units
+    if fmt == "mxfp4":
+        assert ((units >= 3.5) & (units < 7.0)).all()
+    else:  # e4m3 rounding of the group scale moves the maximum by at most 1/16 from 6
+        assert ((units > 6 / 1.07) & (units < 6 * 1.07)).all()
+
+
+@pytest.mark.parametrize("fmt", ["mxfp4", "nvfp4"])
+def test_fp4_technique_gptq_and_save(tmp_path, fmt):
+    model = tiny_model()
+    cal = torch.randint(0, 1024, (2, 32), generator=torch.Generator().manual_seed(3))
+    eff = eco.apply(model, QuantConfig(format=fmt, method="gptq", calibration_tokens=32), calibration=cal)
+    qw = eff.model.layers[0].wqkv
+    assert isinstance(qw, QWeight) and qw.fmt == fmt
+    p = prompts((17,))[0]
+    out = eff.decode(p, 8).tokens
+    assert torch.equal(out, reference_greedy(eff.model, p, 8))
+    eff.save_pretrained(tmp_path / "q")
+    back = eco.load(tiny_model(), tmp_path / "q")
+    assert torch.equal(back.model.layers[0].wqkv.qweight, qw.qweight)
+    assert torch.equal(back.decode(p, 8).tokens, out)
+    with pytest.raises(eco.ConfigError, match="FP4"):
+        QuantConfig(format=fmt, method="hqq")
