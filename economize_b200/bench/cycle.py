@@ -4,7 +4,10 @@ Builds the random-init Llama-3.1-8B architecture and an (untrained, early-exit-i
 times whole ``generate`` calls (CUDA events) for the chosen drafting mode and reports milliseconds per cycle and
 per generated token. The drafter is untrained, so the accepted length is close to one token per cycle; the number
 to read is the cycle time, which bounds tokens per second for any acceptance rate. ``--cycles-only`` stops after
-the warm-up generation (the case a launch-list capture profiles).
+the warm-up generation (the case a launch-list capture profiles). ``--breakdown`` records one more generation with
+the PyTorch profiler (CUPTI kernel records, graph replays included) and prints device microseconds and launches per
+cycle for every kernel name; run it with ``ECZ_PDL=0`` so that no kernel's record includes the time it waits for its
+predecessor (with programmatic dependent launch a kernel starts before the previous one ends).
 """
 
 from __future__ import annotations
@@ -31,6 +34,8 @@ def main(argv: list[str] | None = None) -> None:
     p.add_argument("--iters", type=int, default=3)
     p.add_argument("--layers", type=int, default=32)
     p.add_argument("--cycles-only", action="store_true")
+    p.add_argument("--breakdown", type=int, default=0, metavar="N",
+                   help="print the N kernels with the most device time per cycle (PyTorch profiler)")
     a = p.parse_args(argv)
     cfg = llama31_8b()
     cfg.num_layers = a.layers
@@ -61,11 +66,36 @@ def main(argv: list[str] | None = None) -> None:
     cycles = max(int(r.cycles) for r in res)
     ms = min(times)
     tokens = sum(int(r.tokens.numel()) for r in res)
+    if a.breakdown:
+        _breakdown(eff, prompts, a.new_tokens, dc, a.breakdown)
     print(json.dumps({"mode": a.mode, "batch": a.batch, "prompt_len": a.prompt_len, "new_tokens": a.new_tokens,
                       "layers": a.layers, "ms_per_generate": round(ms, 2), "cycles": cycles,
                       "ms_per_cycle_incl_prefill": round(ms / max(cycles, 1), 3),
                       "tokens_per_s": round(tokens / ms * 1e3, 1),
                       "mean_accepted": round(sum(r.mean_accepted for r in res) / len(res), 3)}))
+
+
+def _breakdown(eff, prompts, new_tokens: int, dc, top: int) -> None:
+    from torch.profiler import ProfilerActivity, profile
+
+    engine = eff.decoder(dc)
+    before = engine.stats.cycles
+    with profile(activities=[ProfilerActivity.CUDA]) as prof:
+        eff.decode_batch(prompts, new_tokens, decoding=dc)
+        torch.cuda.synchronize()
+    cycles = max(1, engine.stats.cycles - before)
+    rows = []
+    for e in prof.key_averages():
+        t = getattr(e, "self_device_time_total", 0) or getattr(e, "self_cuda_time_total", 0)
+        if t > 0:
+            rows.append((t, e.count, e.key))
+    rows.sort(reverse=True)
+    total = sum(r[0] for r in rows)
+    print(json.dumps({"cycles": cycles, "kernel_us_per_cycle": round(total / cycles, 1),
+                      "launches_per_cycle": round(sum(r[1] for r in rows) / cycles, 1)}))
+    for t, n, name in rows[:top]:
+        print(json.dumps({"kernel": name[:120], "us_per_cycle": round(t / cycles, 1),
+                          "launches_per_cycle": round(n / cycles, 2), "share": round(t / total, 4)}))
 
 
 if __name__ == "__main__":

@@ -67,10 +67,13 @@ def bench_gemm(a) -> None:
         ops.linear(x, ws[0])
         torch.cuda.synchronize()
         return
-    ours = time_graph([lambda w=w: ops.linear(x, w) for w in ws], a.iters, a.warmup)
+    # --parts: the split-K kernel whose fp32 partials a fused consumer (norm, SwiGLU, RoPE) reduces, as decode runs it
+    fn = (lambda w: ops.linear_parts(x, w)) if a.parts else (lambda w: ops.linear(x, w))
+    ours = time_graph([lambda w=w: fn(w) for w in ws], a.iters, a.warmup)
     base = time_graph([lambda w=w: torch.matmul(x, w.t()) for w in ws], a.iters, a.warmup)
     nbytes = 2 * (a.m * a.k + a.n * a.k + a.m * a.n)
-    _report("gemm", {"M": a.m, "N": a.n, "K": a.k, "copies": n_copies}, ours, nbytes, 2 * a.m * a.n * a.k, base)
+    _report("gemm_parts" if a.parts else "gemm", {"M": a.m, "N": a.n, "K": a.k, "copies": n_copies}, ours, nbytes,
+            2 * a.m * a.n * a.k, base)
 
 
 def bench_gemm_wq(a) -> None:
@@ -179,6 +182,22 @@ def bench_teal(a) -> None:
             nbytes, 2 * a.m * a.n * a.k * kept, dense)
 
 
+def bench_topk(a) -> None:
+    """Fused log-softmax + top-k over ``[m, n]`` fp32 logits (draft-tree expansion) vs torch's three kernels."""
+    from .. import ops
+
+    dev = torch.device("cuda")
+    xs = [torch.randn(a.m, a.n, device=dev) for _ in range(_copies(4 * a.m * a.n))]
+    d2t = torch.randint(0, 100000, (a.n,), device=dev)  # a draft-to-target id map, as EAGLE-3 heads use
+    if a.once:
+        ops.topk_logp(xs[0], a.topk, -1e4, d2t)
+        torch.cuda.synchronize()
+        return
+    ours = time_graph([lambda x=x: ops.topk_logp(x, a.topk, -1e4, d2t) for x in xs], a.iters, a.warmup)
+    base = time_graph([lambda x=x: torch.log_softmax(x, -1).topk(a.topk, -1) for x in xs], a.iters, a.warmup)
+    _report("topk_logp", {"rows": a.m, "V": a.n, "k": a.topk}, ours, 4 * a.m * a.n, 0, base)
+
+
 def bench_glu(a) -> None:
     from .. import ops
     from ..ops._ext import require
@@ -207,10 +226,12 @@ def bench_glu(a) -> None:
 
 def main(argv: list[str] | None = None) -> None:
     p = argparse.ArgumentParser(description=__doc__.splitlines()[0])
-    p.add_argument("op", choices=["gemm", "gemm_wq", "attention", "layer", "teal", "glu"])
+    p.add_argument("op", choices=["gemm", "gemm_wq", "attention", "layer", "teal", "glu", "topk"])
+    p.add_argument("--topk", type=int, default=10)
     p.add_argument("--m", type=int, default=61)
     p.add_argument("--n", type=int, default=6144)
     p.add_argument("--k", type=int, default=4096)
+    p.add_argument("--parts", action="store_true", help="gemm: time the split-K partials kernel of decode")
     p.add_argument("--fmt", default="int4", choices=["int2", "int4", "int8", "fp8", "mxfp4", "nvfp4"])
     p.add_argument("--group", type=int, default=128)
     p.add_argument("--batch", type=int, default=1)
@@ -223,7 +244,7 @@ def main(argv: list[str] | None = None) -> None:
     p.add_argument("--once", action="store_true", help="one untimed call (for profiler captures)")
     a = p.parse_args(argv)
     {"gemm": bench_gemm, "gemm_wq": bench_gemm_wq, "attention": bench_attention, "layer": bench_layer,
-     "teal": bench_teal, "glu": bench_glu}[a.op](a)
+     "teal": bench_teal, "glu": bench_glu, "topk": bench_topk}[a.op](a)
 
 
 if __name__ == "__main__":

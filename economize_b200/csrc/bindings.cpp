@@ -62,6 +62,24 @@ int* split_counters(const at::Device& device, cudaStream_t stream) {
   return it->second.data_ptr<int>();
 }
 
+// Arrival counters of kernels whose last CTA finishes a reduction (zeroed once; every such kernel leaves them
+// zero), one buffer per device, stream and user: 0 = split top-k (per row).
+constexpr int kCounterInts[1] = {1024};
+
+int* arrival_counters(const at::Device& device, cudaStream_t stream, int which) {
+  static std::mutex mu;
+  static std::unordered_map<uint64_t, Tensor> bufs;
+  std::lock_guard<std::mutex> lock(mu);
+  const uint64_t key = ((static_cast<uint64_t>(device.index()) << 56) ^ reinterpret_cast<uint64_t>(stream)) * 4 +
+                       static_cast<uint64_t>(which);
+  auto it = bufs.find(key);
+  if (it == bufs.end()) {
+    it = bufs.emplace(key, at::zeros({kCounterInts[which]}, at::TensorOptions().dtype(at::kInt).device(device)))
+             .first;
+  }
+  return it->second.data_ptr<int>();
+}
+
 // LRU cache of tensor maps keyed by (base, element size, shape, stride, box, swizzle).
 struct MapKey {
   uintptr_t base;
@@ -264,11 +282,12 @@ Tensor attention(Tensor q, Tensor k_cache, Tensor v_cache, Tensor kv_len, Tensor
                               : tensor_map(k_cache.data_ptr(), rows, D, D, 128);
   const CUtensorMap* tv = fp8 ? tensor_map_ex(v_cache.data_ptr(), 1, rows, D, D, D, 128, 0)
                               : tensor_map(v_cache.data_ptr(), rows, D, D, 128);
+  cudaStream_t stream = at::cuda::getCurrentCUDAStream();
   const int rc = ecz::launch_attention(q.data_ptr(), tk, tv, out.data_ptr(),
                                        plan.ws_floats > 0 ? ws.data_ptr<float>() : nullptr, kv_len.data_ptr<int>(),
                                        n_new.data_ptr<int>(), mask_ptr, B, T, H, Hkv, D, S,
                                        static_cast<float>(scale), static_cast<int>(q_offset), plan,
-                                       status_word(q.device()), at::cuda::getCurrentCUDAStream(),
+                                       status_word(q.device()), stream,
                                        trace.has_value() ? reinterpret_cast<unsigned long long*>(
                                                                trace->data_ptr<int64_t>())
                                                          : nullptr,
@@ -534,9 +553,17 @@ std::tuple<Tensor, Tensor> topk_logp(Tensor logits, int64_t k, double floor_v, c
     CHECK_I64(*d2t);
     TORCH_CHECK(d2t->numel() == V, "d2t must have one entry per logit");
   }
+  cudaStream_t stream = at::cuda::getCurrentCUDAStream();
+  const int splits = rows <= 1024 ? ecz::topk_splits(rows, V, num_sms(logits.get_device())) : 1;
+  Tensor ws;
+  if (splits > 1) {
+    ws = at::empty({static_cast<int64_t>(ecz::topk_workspace_bytes(rows, splits))}, logits.options().dtype(at::kByte));
+  }
   const int rc = ecz::launch_topk_logp(logits.data_ptr<float>(), d2t.has_value() ? d2t->data_ptr<int64_t>() : nullptr,
                                        vals.data_ptr<float>(), ids.data_ptr<int64_t>(), rows, V, static_cast<int>(k),
-                                       static_cast<float>(floor_v), at::cuda::getCurrentCUDAStream());
+                                       static_cast<float>(floor_v), stream, splits,
+                                       splits > 1 ? ws.data_ptr() : nullptr,
+                                       splits > 1 ? arrival_counters(logits.device(), stream, 0) : nullptr);
   TORCH_CHECK(rc == 0, "topk_logp: 1 <= k <= 16");
   return {vals, ids};
 }
@@ -932,6 +959,25 @@ void tree_expand(Tensor c_vals, Tensor c_ids, Tensor f_scores, Tensor f_cand, Te
   TORCH_CHECK(rc == 0, "tree_expand: k <= 16 and (d + 1) k <= 64");
 }
 
+// Ancestor bits [B, T] int64 and positions kv_len + depth [B, T] int32 of a verified tree given by its parents.
+std::tuple<Tensor, Tensor> tree_layout(Tensor parents, Tensor kv_len) {
+  CHECK_CUDA(parents);
+  CHECK_ON(kv_len, parents);
+  CHECK_I64(parents);
+  CHECK_I32(kv_len);
+  TORCH_CHECK(parents.dim() == 2 && parents.size(1) >= 1 && parents.size(1) <= 64, "tree_layout: parents [B, T <= 64]");
+  c10::cuda::CUDAGuard guard(parents.device());
+  parents = parents.contiguous();
+  const int B = static_cast<int>(parents.size(0)), T = static_cast<int>(parents.size(1));
+  TORCH_CHECK(kv_len.numel() == B && kv_len.is_contiguous(), "tree_layout: kv_len [B]");
+  auto bits = at::empty({B, T}, parents.options());
+  auto pos = at::empty({B, T}, parents.options().dtype(at::kInt));
+  const int rc = ecz::launch_tree_layout(parents.data_ptr<int64_t>(), kv_len.data_ptr<int>(), bits.data_ptr<int64_t>(),
+                                         pos.data_ptr<int>(), B, T, at::cuda::getCurrentCUDAStream());
+  TORCH_CHECK(rc == 0, "tree_layout: launch failed");
+  return {bits, pos};
+}
+
 std::tuple<Tensor, Tensor> tree_select(Tensor cand_tokens, Tensor cand_scores, Tensor cand_parents, int64_t k,
                                        int64_t total) {
   CHECK_CUDA(cand_tokens);
@@ -1188,6 +1234,8 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("rejection", &rejection, "lossless speculative sampling of a draft chain (accept/reject + resample)");
   m.def("ngram", &ngram, "prompt-lookup draft proposals from the token history");
   m.def("tree_expand", &tree_expand, "one depth of dynamic-tree drafting bookkeeping (in place)");
+  m.def("tree_layout", &tree_layout, "ancestor bits and positions of a verified tree", py::arg("parents"),
+        py::arg("kv_len"));
   m.def("tree_select", &tree_select, "the best candidates of a draft tree in candidate order, parents remapped");
   m.def("sign_matvec", &sign_matvec, "x times a packed sign matrix (LittleBit factors, <= 16 rows)");
   m.def("colsparse_linear", &colsparse_linear, "activation-sparse GEMV over a transposed weight (<= 16 rows)");

@@ -92,7 +92,11 @@ int launch_attention_scores(const void* q, const CUtensorMap* tm_k, const float*
 
 // sampling.cu
 int launch_topk_logp(const float* logits, const int64_t* d2t, float* vals, int64_t* ids, int rows, int V, int k,
-                     float floor_v, cudaStream_t stream);
+                     float floor_v, cudaStream_t stream, int splits = 1, void* workspace = nullptr,
+                     int* counters = nullptr);
+// chunks per row of the split top-k (1: one CTA per row) and its workspace; counters: `rows` zeroed ints
+int topk_splits(int rows, int V, int num_sms);
+size_t topk_workspace_bytes(int rows, int splits);
 int launch_sample(const float* probs, const float* u, int64_t* out, int rows, int V, cudaStream_t stream);
 int launch_rejection(const float* p, const float* q, const int64_t* drafts, const float* u_acc, const float* u_draw,
                      int* n_acc, int64_t* out, int B, int k, int V, cudaStream_t stream);
@@ -162,6 +166,8 @@ int launch_tree_expand(const float* c_vals, const int64_t* c_ids, float* f_score
                        int n_cand, int n_fwd, bool next, cudaStream_t stream);
 int launch_tree_select(const int64_t* cand_tokens, const float* cand_scores, const int64_t* cand_parents, int B,
                        int n_cand, int k, int total, int64_t* out_tokens, int64_t* out_parents, cudaStream_t stream);
+int launch_tree_layout(const int64_t* parents, const int* kv_len, int64_t* bits, int* positions, int B, int T,
+                       cudaStream_t stream);
 
 // ep.cu: expert-parallel dispatch / combine over IPC-mapped symmetric buffers (layout below, per rank).
 struct EpLayout {

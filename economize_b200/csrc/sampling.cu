@@ -229,6 +229,7 @@ __global__ void __launch_bounds__(kTopThreads) topk_logp_kernel(const float* __r
     Cand lst[K];
 #pragma unroll
     for (int j = 0; j < K; ++j) lst[j] = (lane < kTopThreads / 32 && j < k) ? wl[lane][j] : Cand{-INFINITY, 0x7fffffff};
+    Cand win{-INFINITY, 0};
     for (int r = 0; r < k; ++r) {
       const Cand c = lst[0];
       Cand best = c;
@@ -238,16 +239,146 @@ __global__ void __launch_bounds__(kTopThreads) topk_logp_kernel(const float* __r
         if (better(o, best)) best = o;
       }
       if (c.i == best.i && c.v == best.v) list_pop(lst);
-      if (lane == 0) {
-        const size_t o = static_cast<size_t>(blockIdx.x) * k + r;
-        vals[o] = fmaxf(best.v - lse, floor_v);
-        ids[o] = d2t != nullptr ? best.i + d2t[best.i] : best.i;
+      if (lane == r) win = best;  // lane r keeps the r-th winner
+    }
+    if (lane < k) {  // all k id-map loads in flight at once
+      const size_t o = static_cast<size_t>(blockIdx.x) * k + lane;
+      vals[o] = fmaxf(win.v - lse, floor_v);
+      ids[o] = d2t != nullptr ? win.i + d2t[win.i] : win.i;
+    }
+  }
+}
+
+// ---- split variant: rows too few to fill the GPU ------------------------------------------------------------------
+// Grid (rows, S): CTA (r, s) scans chunk s of row r for its max, rescaled sum of exponentials and top-k, and writes
+// them to the workspace; the last CTA of a row to finish (a per-row arrival counter, reset by that CTA for the next
+// launch) merges the S partial results into the row's log-sum-exp and top-k. Same outputs as topk_logp_kernel: the
+// candidates are compared by (value, index) everywhere, so the merged top-k is the row's top-k.
+constexpr int kSplitThreads = 256;
+
+template <int K>
+__global__ void __launch_bounds__(kSplitThreads) topk_logp_split_kernel(
+    const float* __restrict__ logits, const int64_t* __restrict__ d2t, float* __restrict__ vals,
+    int64_t* __restrict__ ids, Cand* __restrict__ ws_cands, float2* __restrict__ ws_stats, int* __restrict__ counters,
+    int V, int k, int chunk, float floor_v) {
+  pdl_trigger();
+  pdl_wait();
+  const int r = blockIdx.x, s = blockIdx.y, S = gridDim.y;
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  constexpr int kWarps = kSplitThreads / 32;
+  __shared__ float red[2 * kWarps];
+  __shared__ Cand wl[kWarps][K];
+  __shared__ int is_last;
+  const float* row = logits + static_cast<size_t>(r) * V;
+  const int lo = s * chunk, hi = min(V, lo + chunk);
+  Cand mine[K];
+#pragma unroll
+  for (int j = 0; j < K; ++j) mine[j] = Cand{-INFINITY, 0x7fffffff};
+  float mx = -INFINITY, se = 0.f;
+  for (int i = lo + tid; i < hi; i += kSplitThreads) {
+    const float x = __ldg(row + i);
+    if (x > mx) {
+      se = se * __expf(mx - x) + 1.f;
+      mx = x;
+    } else if (x != -INFINITY) {
+      se += __expf(x - mx);
+    }
+    list_insert(mine, Cand{x, i});
+  }
+  float wmx = warp_max(mx);
+  float wse = warp_sum(mx == -INFINITY ? 0.f : se * __expf(mx - wmx));
+  if (lane == 0) {
+    red[warp] = wmx;
+    red[kWarps + warp] = wse;
+  }
+  warp_merge(mine, k, wl[warp]);
+  __syncthreads();
+  Cand* out_c = ws_cands + (static_cast<size_t>(r) * S + s) * K;
+  if (warp == 0) {
+    const float m_l = lane < kWarps ? red[lane] : -INFINITY;
+    const float bmx = warp_max(m_l);
+    const float s_l = lane < kWarps && m_l != -INFINITY ? red[kWarps + lane] * __expf(m_l - bmx) : 0.f;
+    const float bse = warp_sum(s_l);
+    Cand lst[K];
+#pragma unroll
+    for (int j = 0; j < K; ++j) lst[j] = (lane < kWarps && j < k) ? wl[lane][j] : Cand{-INFINITY, 0x7fffffff};
+    warp_merge(lst, k, out_c);
+    if (lane == 0) ws_stats[static_cast<size_t>(r) * S + s] = make_float2(bmx, bse);
+    __threadfence();
+    __syncwarp();
+    if (lane == 0) {
+      const int prev = atomicAdd(&counters[r], 1);
+      is_last = prev == S - 1;
+      if (is_last) counters[r] = 0;  // ready for the next launch
+    }
+  }
+  __syncthreads();
+  if (!is_last) return;
+  __threadfence();
+  // ---- merge the row's S partial results ----
+  const Cand* row_c = ws_cands + static_cast<size_t>(r) * S * K;
+  const float2* row_s = ws_stats + static_cast<size_t>(r) * S;
+#pragma unroll
+  for (int j = 0; j < K; ++j) mine[j] = Cand{-INFINITY, 0x7fffffff};
+  // the other CTAs' results are read from L2 (ld.global.cg): this SM's L1 may not have seen their stores
+  for (int i = tid; i < S * k; i += kSplitThreads) {
+    const Cand* src = row_c + (i / k) * K + i % k;
+    list_insert(mine, Cand{__ldcg(&src->v), __ldcg(&src->i)});
+  }
+  float m2 = -INFINITY;
+  for (int i = tid; i < S; i += kSplitThreads) m2 = fmaxf(m2, __ldcg(&row_s[i].x));
+  m2 = warp_max(m2);
+  if (lane == 0) red[warp] = m2;
+  __syncthreads();
+  float rmx = lane < kWarps ? red[lane] : -INFINITY;
+  rmx = warp_max(rmx);
+  float s2 = 0.f;
+  for (int i = tid; i < S; i += kSplitThreads) {
+    const float2 st = __ldcg(&row_s[i]);
+    if (st.x != -INFINITY) s2 += st.y * __expf(st.x - rmx);
+  }
+  s2 = warp_sum(s2);
+  __syncthreads();
+  if (lane == 0) red[kWarps + warp] = s2;
+  warp_merge(mine, k, wl[warp]);
+  __syncthreads();
+  if (warp == 0) {
+    const float lse = rmx + __logf(warp_sum(lane < kWarps ? red[kWarps + lane] : 0.f));
+    Cand lst[K];
+#pragma unroll
+    for (int j = 0; j < K; ++j) lst[j] = (lane < kWarps && j < k) ? wl[lane][j] : Cand{-INFINITY, 0x7fffffff};
+    Cand win{-INFINITY, 0};
+    for (int q = 0; q < k; ++q) {
+      const Cand c = lst[0];
+      Cand best = c;
+#pragma unroll
+      for (int off = 16; off > 0; off >>= 1) {
+        const Cand o{__shfl_xor_sync(0xffffffffu, best.v, off), __shfl_xor_sync(0xffffffffu, best.i, off)};
+        if (better(o, best)) best = o;
       }
+      if (c.i == best.i && c.v == best.v) list_pop(lst);
+      if (lane == q) win = best;
+    }
+    if (lane < k) {
+      const size_t o = static_cast<size_t>(r) * k + lane;
+      vals[o] = fmaxf(win.v - lse, floor_v);
+      ids[o] = d2t != nullptr ? win.i + d2t[win.i] : win.i;
     }
   }
 }
 
 }  // namespace
+
+// Chunks per row for the split top-k: enough CTAs for two per SM, each chunk at least 512 logits, at most 64.
+int topk_splits(int rows, int V, int num_sms) {
+  if (rows <= 0 || rows >= num_sms) return 1;
+  const int want = (2 * num_sms + rows - 1) / rows;
+  return std::max(1, std::min(std::min(want, 64), V / 512));
+}
+
+size_t topk_workspace_bytes(int rows, int splits) {
+  return static_cast<size_t>(rows) * splits * (kMaxTopK * sizeof(Cand) + sizeof(float2));
+}
 
 int launch_sample(const float* probs, const float* u, int64_t* out, int rows, int V, cudaStream_t stream) {
   if (rows == 0) return 0;
@@ -263,9 +394,27 @@ int launch_rejection(const float* p, const float* q, const int64_t* drafts, cons
 }
 
 int launch_topk_logp(const float* logits, const int64_t* d2t, float* vals, int64_t* ids, int rows, int V, int k,
-                     float floor_v, cudaStream_t stream) {
+                     float floor_v, cudaStream_t stream, int splits, void* workspace, int* counters) {
   if (k < 1 || k > kMaxTopK || k > V) return -1;
   if (rows == 0) return 0;
+  if (splits > 1) {
+    if (workspace == nullptr || counters == nullptr) return -2;
+    Cand* wc = static_cast<Cand*>(workspace);
+    float2* wsst = reinterpret_cast<float2*>(wc + static_cast<size_t>(rows) * splits * kMaxTopK);
+    const int chunk = (V + splits - 1) / splits;
+    const dim3 grid(rows, splits);
+    if (k <= 4) {
+      launch_pdl(topk_logp_split_kernel<4>, grid, dim3(kSplitThreads), 0, stream, logits, d2t, vals, ids, wc, wsst,
+                 counters, V, k, chunk, floor_v);
+    } else if (k <= 8) {
+      launch_pdl(topk_logp_split_kernel<8>, grid, dim3(kSplitThreads), 0, stream, logits, d2t, vals, ids, wc, wsst,
+                 counters, V, k, chunk, floor_v);
+    } else {
+      launch_pdl(topk_logp_split_kernel<16>, grid, dim3(kSplitThreads), 0, stream, logits, d2t, vals, ids, wc, wsst,
+                 counters, V, k, chunk, floor_v);
+    }
+    return 0;
+  }
   if (k <= 4) {
     launch_pdl(topk_logp_kernel<4>, dim3(rows), dim3(kTopThreads), 0, stream, logits, d2t, vals, ids, V, k, floor_v);
   } else if (k <= 8) {

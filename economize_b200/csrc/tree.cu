@@ -6,6 +6,8 @@
 //                       origin of every frontier node (for the state gather) are computed
 //   tree_select_kernel  the `total` best candidates (key = score - 1e-9 depth in double, ties to the lower index)
 //                       in candidate order, with every parent mapped to its position among them
+//   tree_layout_kernel  the verified tree's ancestor bits and token positions from its parents (every drafting
+//                       mode), in place of pointer doubling and a bit count in tensor operations
 //
 // Both replace chains of small tensor operations that a captured cycle would otherwise launch one by one.
 #include <algorithm>
@@ -110,7 +112,40 @@ __global__ void __launch_bounds__(512) tree_select_kernel(const int64_t* __restr
   }
 }
 
+// parents [B, T] (parents[b, i] < i for i >= 1; node 0 is the root): bits[b, i] has bit j set when node j is i or
+// one of its ancestors, positions[b, i] = kv_len[b] + depth(i). One CTA of T threads per row; thread i walks up its
+// ancestor chain in shared memory (at most T - 1 steps, so a malformed row cannot loop).
+__global__ void __launch_bounds__(64) tree_layout_kernel(const int64_t* __restrict__ parents,
+                                                         const int* __restrict__ kv_len, int64_t* __restrict__ bits,
+                                                         int* __restrict__ positions, int T) {
+  pdl_trigger();
+  pdl_wait();
+  const int b = blockIdx.x, i = threadIdx.x;
+  __shared__ int par[64];
+  if (i < T) par[i] = static_cast<int>(parents[static_cast<size_t>(b) * T + i]);
+  __syncthreads();
+  if (i >= T) return;
+  uint64_t m = 1ull << i;
+  int depth = 0;
+  for (int j = i, steps = 0; j > 0 && steps < T; ++steps) {
+    const int p = par[j];
+    j = (p >= 0 && p < j) ? p : 0;  // parents precede their children; anything else ends the walk at the root
+    m |= 1ull << j;
+    ++depth;
+  }
+  bits[static_cast<size_t>(b) * T + i] = static_cast<int64_t>(m);
+  positions[static_cast<size_t>(b) * T + i] = kv_len[b] + depth;
+}
+
 }  // namespace
+
+int launch_tree_layout(const int64_t* parents, const int* kv_len, int64_t* bits, int* positions, int B, int T,
+                       cudaStream_t stream) {
+  if (T < 1 || T > 64) return -1;
+  if (B == 0) return 0;
+  launch_pdl(tree_layout_kernel, dim3(B), dim3(64), 0, stream, parents, kv_len, bits, positions, T);
+  return 0;
+}
 
 int launch_tree_expand(const float* c_vals, const int64_t* c_ids, float* f_scores, int64_t* f_cand, int64_t* f_tokens,
                        int64_t* parent_fwd, int64_t* fwd_bits, int64_t* origin, int64_t* bits_next,

@@ -33,7 +33,7 @@ from .drafter import DraftModel
 from .policies import POLICIES, ConfidencePolicy, DynamicTreePolicy, SequoiaPolicy, SpecExecPolicy
 from .sequoia import AcceptanceProfile, StaticPlan, StaticTree, record_cycle
 from .specexec import SearchOptions
-from .tree import LOGP_FLOOR, TreeOptions, ancestor_bits, popcount64, select_candidates
+from .tree import LOGP_FLOOR, TreeOptions, select_candidates
 from .verifiers import VERIFIERS, RejectionVerifier, TypicalVerifier
 
 __all__ = ["DecodeResult", "GenerationStats", "SpecEngine"]
@@ -385,8 +385,7 @@ class SpecEngine:
         tokens = torch.cat([st.last[:, None], draft_tokens], 1)  # [B, T]
         length = tokens.shape[1]
         parents = torch.cat([torch.zeros(batch, 1, dtype=torch.int64, device=dev), draft_parents + 1], 1)
-        bits = ancestor_bits(parents, depth)
-        positions = (st.kv_len[:, None] + (popcount64(bits) - 1)).to(torch.int32)
+        bits, positions = ops.tree_layout(parents, st.kv_len, depth)
         n_new = torch.full((batch,), length, dtype=torch.int32, device=dev)
         sb = StepBatch(st.kv_len, n_new, positions, bits)
         with phase("refresh"):

@@ -35,6 +35,7 @@ __all__ = [
     "rope_store",
     "sample",
     "topk_logp",
+    "tree_layout",
     "silu_mul",
 ]
 
@@ -223,6 +224,17 @@ def ngram(history: torch.Tensor, length: torch.Tensor, k: int, min_n: int, max_n
     if history.is_cuda:
         return require().ngram(history, length.to(torch.int32), int(k), int(min_n), int(max_n), bool(earliest))
     return reference.ngram(history, length, k, min_n, max_n, earliest)
+
+
+def tree_layout(parents: torch.Tensor, kv_len: torch.Tensor, max_depth: int) -> tuple[torch.Tensor, torch.Tensor]:
+    """Ancestor bits ``[B, T]`` (int64) and positions ``kv_len + depth`` ``[B, T]`` (int32) of a verified tree given
+    by ``parents [B, T]`` (root at node 0, ``parents[:, i] < i``); one kernel on CUDA."""
+    if parents.is_cuda:
+        return require().tree_layout(parents.long(), kv_len.int())
+    from ..decoding.tree import ancestor_bits, popcount64
+
+    bits = ancestor_bits(parents, max_depth)
+    return bits, (kv_len[:, None] + (popcount64(bits) - 1)).to(torch.int32)
 
 
 def topk_logp(logits: torch.Tensor, k: int, floor: float, d2t: torch.Tensor | None = None

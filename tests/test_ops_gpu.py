@@ -272,7 +272,8 @@ def test_partials_index_like_the_dense_tensor(cuda):
     assert torch.equal(p[rows, cols].sum(), p.sum()[rows, cols])
 
 
-@pytest.mark.parametrize("rows,V,k", [(1, 32000, 10), (10, 32000, 10), (61, 1024, 16), (3, 128256, 4)])
+@pytest.mark.parametrize("rows,V,k", [(1, 32000, 10), (10, 32000, 10), (61, 1024, 16), (3, 128256, 4),
+                                      (200, 32000, 8)])
 def test_topk_logp_matches_torch(cuda, rows, V, k):
     g = torch.Generator(device=cuda).manual_seed(0)
     logits = torch.randn(rows, V, device=cuda, generator=g) * 3
@@ -281,6 +282,21 @@ def test_topk_logp_matches_torch(cuda, rows, V, k):
     ref = torch.log_softmax(logits, -1).topk(k, -1)
     _close(vals, ref.values, 1e-4, 1e-5)
     assert torch.equal(ids, ref.indices + d2t[ref.indices])
+
+
+def test_topk_logp_split_repeats_and_masked_chunks(cuda):
+    """Rows split over several CTAs: the per-row arrival counters reset themselves, so back-to-back calls agree, and
+    chunks that hold only -inf logits merge correctly."""
+    g = torch.Generator(device=cuda).manual_seed(3)
+    logits = torch.randn(7, 32000, device=cuda, generator=g)
+    logits[:, 4000:30000] = float("-inf")
+    first = ops.topk_logp(logits, 16, -1e4, None)
+    for _ in range(3):
+        again = ops.topk_logp(logits, 16, -1e4, None)
+        assert torch.equal(first[0], again[0]) and torch.equal(first[1], again[1])
+    ref = torch.log_softmax(logits, -1).topk(16, -1)
+    _close(first[0], ref.values, 1e-4, 1e-5)
+    assert torch.equal(first[1], ref.indices)
 
 
 @pytest.mark.gpu
@@ -358,3 +374,18 @@ def test_fused_tree_kernels_match_the_reference(cuda, k, depth, total):
     rtok, rpar = select_candidates(torch.cat(ref_t, 1), torch.cat(ref_s, 1), torch.cat(ref_p, 1), torch.cat(ref_d),
                                    total)
     assert torch.equal(tok, rtok) and torch.equal(par, rpar)
+
+
+def test_tree_layout_matches_pointer_doubling(cuda):
+    from economize_b200.decoding.tree import ancestor_bits, popcount64
+
+    g = torch.Generator().manual_seed(4)
+    for T in (1, 7, 61, 64):
+        parents = torch.zeros(3, T, dtype=torch.int64)
+        for i in range(1, T):
+            parents[:, i] = torch.randint(0, i, (3,), generator=g)
+        kv_len = torch.tensor([5, 0, 700], dtype=torch.int32)
+        bits, pos = ops.tree_layout(parents.to(cuda), kv_len.to(cuda), 63)
+        ref = ancestor_bits(parents, 63)
+        assert torch.equal(bits.cpu(), ref)
+        assert torch.equal(pos.cpu(), (kv_len[:, None] + popcount64(ref) - 1).int())
