@@ -8,7 +8,7 @@
 // side, tokens on N) and inserts a dequantisation stage between TMA and the tensor core:
 //
 //   warp 0      TMA: packed weight tile [128 x 64 K], this group's scales (and zeros) and the activation tile
-//   warps 2-5   one weight row per thread: unpack, subtract the zero, multiply by the scale (bf16x2 arithmetic,
+//   warps 2-9   half a weight row per thread: unpack, subtract the zero, multiply by the scale (bf16x2 arithmetic,
 //               bit-exact with bf16((q - z) * s)), store the 128 x 64 bf16 tile in the 128-byte-swizzled K-major
 //               layout tcgen05 reads, fence the generic->async proxy and arrive on the stage's barrier
 //   warp 1      UMMA issue (4 x K=16 per stage) from the converted tile and the activation tile
@@ -44,8 +44,8 @@ namespace {
 constexpr int kBM = 128;
 constexpr int kBK = 64;
 constexpr int kConvBytes = kBM * kBK * 2;  // one bf16 weight tile
-constexpr int kConvStages = 2;
-constexpr int kThreads = 192;
+constexpr int kDeqWarps = 8;  // two threads per weight row, each converting half of the 64-wide K-block
+constexpr int kThreads = 64 + 32 * kDeqWarps;
 
 template <int FMT>
 struct WqFmt {
@@ -66,7 +66,11 @@ struct WqCfg {
   static constexpr int kXBytes = BN * kBK * 2;
   static constexpr int kLoadBytes = kXBytes + WqFmt<FMT>::kRawBytes + WqFmt<FMT>::kSideBytes + kBM * 2;
   static constexpr int kBudget = (kOcc == 1 ? 200 : 100) * 1024;
+  // converted-tile ring: three deep for decode tiles (the dequant -> MMA -> release round trip bounds a stage),
+  // two for wide token tiles whose activation stages need the room
+  static constexpr int kConvStages = BN <= 64 ? 3 : 2;
   static constexpr int kStages = std::min(8, (kBudget - kConvStages * kConvBytes) / kLoadBytes);
+  static_assert(kStages >= 2, "the load ring needs two stages");
   static constexpr int kTmemCols = BN < 32 ? 32 : BN;
   // layout: conv ring | X ring | raw ring | scale ring | zero ring | barriers
   static constexpr int kXOff = kConvStages * kConvBytes;
@@ -171,6 +175,7 @@ __global__ void __launch_bounds__(kThreads, WqCfg<FMT, BN>::kOcc)
   using Cfg = WqCfg<FMT, BN>;
   using F = WqFmt<FMT>;
   constexpr int S = Cfg::kStages;
+  constexpr int kConvStages = Cfg::kConvStages;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* conv = smem;
@@ -203,7 +208,7 @@ __global__ void __launch_bounds__(kThreads, WqCfg<FMT, BN>::kOcc)
       mbar_init(&empty[s], 1);
     }
     for (int c = 0; c < kConvStages; ++c) {
-      mbar_init(&conv_full[c], 4);  // one arrival per dequantising warp
+      mbar_init(&conv_full[c], kDeqWarps);  // one arrival per dequantising warp
       mbar_init(&conv_empty[c], 1);
     }
     mbar_init(accum, 1);
@@ -271,8 +276,9 @@ __global__ void __launch_bounds__(kThreads, WqCfg<FMT, BN>::kOcc)
     }
     umma_commit(accum);
   } else if (nkb > 0 && warp >= 2) {
-    // ---- dequantisation: thread t converts weight row t of every stage ----
-    const int row = threadIdx.x - 64;
+    // ---- dequantisation: thread t converts chunks 4h .. 4h + 3 (h = t / 128, warp-uniform) of weight row t % 128
+    const int row = (threadIdx.x - 64) & (kBM - 1);
+    const int half = (threadIdx.x - 64) / kBM;
     for (int kb = 0; kb < nkb; ++kb) {
       const int s = kb % S, c = kb % kConvStages;
       if (!mbar_wait(&full[s], (kb / S) & 1u, status, kStatusWaitFull, abort_flag)) break;
@@ -293,14 +299,17 @@ __global__ void __launch_bounds__(kThreads, WqCfg<FMT, BN>::kOcc)
       }
       const uint4* raw_row = reinterpret_cast<const uint4*>(raw + s * F::kRawBytes + row * F::kRawRowBytes);
       uint32_t words[F::kRawRowBytes / 4];
+      constexpr int kVecs = F::kRawRowBytes / 16;
 #pragma unroll
-      for (int i = 0; i < F::kRawRowBytes / 16; ++i) {
+      for (int i = 0; i < kVecs; ++i) {
+        if (kVecs > 1 && i * 2 / kVecs != half) continue;  // only this half's codes (int2 rows are one vector)
         const uint4 v = raw_row[i];
         words[4 * i] = v.x; words[4 * i + 1] = v.y; words[4 * i + 2] = v.z; words[4 * i + 3] = v.w;
       }
       uint8_t* dst_row = conv + c * kConvBytes + row * 128;
 #pragma unroll
       for (int j = 0; j < 8; ++j) {
+        if ((j >> 2) != half) continue;  // uniform per warp; j stays a compile-time index into `words`
         uint4 v;
         if constexpr (FMT == kWqSp24) {
           v = expand_sp24(words, meta, j);
@@ -323,11 +332,12 @@ __global__ void __launch_bounds__(kThreads, WqCfg<FMT, BN>::kOcc)
   __syncthreads();
   tc_fence_after();
   const bool ok = nkb > 0 && !*abort_flag;
+  const bool epi = warp >= 2 && warp < 6;  // the epilogue warps: one per TMEM lane quarter
   const int quarter = warp & 3;  // TMEM lanes 32 * (warp % 4) .. + 31 belong to this warp
   const uint32_t lane_base = tmem + (static_cast<uint32_t>(quarter * 32) << 16);
   const int feat = quarter * 32 + lane;
   if (splits == 1) {
-    if (ok && warp >= 2) {
+    if (ok && epi) {
 #pragma unroll 1
       for (int c = 0; c < BN; c += 16) {
         float v[16];
@@ -343,7 +353,7 @@ __global__ void __launch_bounds__(kThreads, WqCfg<FMT, BN>::kOcc)
       }
     }
   } else {
-    if (warp >= 2) {
+    if (epi) {
 #pragma unroll 1
       for (int c = 0; c < BN; c += 16) {
         float v[16];
@@ -353,7 +363,7 @@ __global__ void __launch_bounds__(kThreads, WqCfg<FMT, BN>::kOcc)
       }
     }
     cluster_sync();
-    if (warp >= 2) {
+    if (epi) {
       const int t = threadIdx.x - 64;
       const int cg = t & 31, rp = t >> 5;
       const int n = n0 + cg * 4;
@@ -432,8 +442,8 @@ int gemm_wq_splits(int M, int N, int K, int fmt, int num_sms) {
   const int slots = gemm_block_n(M) <= 64 ? 2 * num_sms : num_sms;
   const int tiles = ((N + kBM - 1) / kBM) * ((M + gemm_block_n(M) - 1) / gemm_block_n(M));
   const int kb = K / kBK;
-  // at least 8 K-blocks (512 K) per CTA for int8/fp8, 16 for int4: below that the prologue dominates
-  const int min_kb = fmt == kWqInt2 ? 32 : (fmt == kWqInt4 || fmt == kWqMxfp4 || fmt == kWqNvfp4) ? 16 : 8;
+  // at least 8 K-blocks (512 K) per CTA (16 for int2): below that the prologue dominates
+  const int min_kb = fmt == kWqInt2 ? 16 : 8;
   int splits = std::max(1, std::min(slots / std::max(1, tiles), kb / min_kb));
   return std::min(8, splits);
 }
