@@ -63,6 +63,10 @@ class EarlyExitTechnique(SelfDraftTechnique):
         elif config.adaptation == "lora":
             self.head_lora = LoRAWeight(model.head_weight, config.lora_rank, config.lora_alpha)
 
+    def lora_targets(self) -> dict:
+        """The low-rank adapters by Hugging Face module name (``adaptation="lora"``: the readout ``lm_head``)."""
+        return {"lm_head": self.head_lora} if self.config.adaptation == "lora" else {}
+
     def view_layers(self) -> list[int]:
         k = self.config.exit_layer or max(1, self.model.config.num_layers // 2)
         return list(range(k))
