@@ -131,3 +131,44 @@ def test_depth_methods_run_in_cuda_graphs(cuda, cfg):
         assert all(torch.equal(a.tokens.cpu(), b.tokens.cpu()) for a, b in zip(base, out))
     else:
         assert em.techniques[cfg.technique].depth_stats()["layer_tokens_entered"] > 0
+
+
+def test_hoeffding_bentkus_and_fixed_sequence_testing():
+    from economize_b200.techniques.dynamic_depth import hoeffding_bentkus_pvalue, ltt_threshold, token_mismatch
+
+    assert hoeffding_bentkus_pvalue(0.0, 200, 0.1) < 1e-6  # no loss on many examples: risk > 0.1 is implausible
+    assert hoeffding_bentkus_pvalue(0.2, 200, 0.1) == 1.0  # mean above epsilon: cannot reject
+    ps = [hoeffding_bentkus_pvalue(m, 100, 0.2) for m in (0.0, 0.05, 0.1, 0.15)]
+    assert ps == sorted(ps)  # a larger mean loss gives a larger p-value
+    cands = [0.2, 0.4, 0.6, 0.8]
+    losses = [[0.5] * 100, [0.0] * 100, [0.0] * 100, [0.0] * 100]  # 0.2 fails; 0.4 and above pass
+    assert ltt_threshold(cands, losses, delta=0.05, epsilon=0.1) == 0.4
+    gap = [[0.0] * 100, [0.5] * 100, [0.0] * 100, [0.0] * 100]  # the walk stops at the first failure (0.4)
+    assert ltt_threshold(cands, gap, delta=0.05, epsilon=0.1) == 0.6
+    assert ltt_threshold(cands, [[0.5] * 10] * 4, delta=0.05, epsilon=0.1) == 1.0
+    assert token_mismatch(torch.tensor([1, 2, 3]), torch.tensor([1, 5, 3, 4])) == 0.5
+
+
+def test_calm_calibration_restores_config_and_certifies():
+    from economize_b200.techniques.dynamic_depth import calibrate_threshold
+
+    em = eco.apply(tiny_model(), CalmConfig(confidence="state", threshold=0.3))
+    lam = calibrate_threshold(em, prompts(), 8, delta=0.2, epsilon=0.5, candidates=(0.5, 0.9, 0.999))
+    assert lam in (0.5, 0.9, 0.999, 1.0)
+    assert em.techniques["calm"].config.threshold == 0.3
+
+
+def test_free_beta_mixture_threshold():
+    from economize_b200.techniques.dynamic_depth import beta_moments, bmm_threshold, free_calibration_pairs
+
+    g = torch.Generator().manual_seed(0)
+    a, b = beta_moments(torch.distributions.Beta(torch.tensor(8.0), torch.tensor(2.0)).sample((20000,)))
+    assert abs(a - 8.0) < 0.5 and abs(b - 2.0) < 0.2
+    conf = torch.cat([torch.rand(500, generator=g) * 0.5, 0.5 + torch.rand(500, generator=g) * 0.5])
+    agree = torch.arange(1000) >= 500  # confident tokens agree, unsure ones do not
+    lam = bmm_threshold(conf, agree, posterior=0.5)
+    assert 0.35 <= lam <= 0.65
+    assert bmm_threshold(conf, torch.ones(1000, dtype=torch.bool)) == 0.9  # one class only: the default
+    em = eco.apply(tiny_model(), FreeConfig(exit_layer=2))
+    c, ok = free_calibration_pairs(em, prompts()[0][None])
+    assert c.shape == ok.shape == (17,) and bool(((c >= 0) & (c <= 1)).all())
