@@ -50,9 +50,15 @@ class SequentialHeadTechnique(Technique):
     def default_decoding(self) -> DecodeConfig:
         return DecodeConfig(cycle_length=min(self.max_steps(), 5) + 1)
 
+    def source_states(self, h: torch.Tensor) -> torch.Tensor:
+        """The states the heads start from, given the target's states ``[B, S, H]`` of a whole sequence (causal);
+        the identity unless a subclass runs a layer of its own over them (Hydra++'s prefix layer)."""
+        return h
+
     # teacher forcing: logits of step j (0-based) at every position t predict token t + j + 2
     def teacher_forced(self, h: torch.Tensor, tokens: torch.Tensor, steps: int) -> list[torch.Tensor]:
         s = tokens.shape[1]
+        h = self.source_states(h)
         out = []
         state = self.start(h[:, : s - 1], self.embed(tokens[:, 1:]))  # position t with token t + 1
         for j in range(steps):

@@ -32,6 +32,8 @@ def plain(model):
 @pytest.mark.parametrize("make,decoding", [
     (lambda: HydraConfig(num_heads=4), None),
     (lambda: HydraConfig(num_heads=4), TREE),
+    (lambda: HydraConfig(num_heads=4, prefix_layer=True), None),
+    (lambda: HydraConfig(num_heads=4, prefix_layer=True, prefix_intermediate_size=128), TREE),
     (lambda: RedrafterConfig(beam_width=4, beam_length=4), None),
     (lambda: RedrafterConfig(beam_length=4), eco.DecodeConfig(cycle_length=4)),
     (lambda: PardConfig(model=tiny_model(num_layers=2, seed=1), max_drafts=4), None),
@@ -55,6 +57,7 @@ def test_pard_self_draft_accepts(model, plain):
 
 
 @pytest.mark.parametrize("cfg,name", [(HydraConfig(num_heads=3), "step_distill"),
+                                      (HydraConfig(num_heads=3, prefix_layer=True), "step_distill"),
                                       (RedrafterConfig(beam_length=3), "step_distill"),
                                       (JumpConfig(target_layer=1, source_layer=2), "jump_rollout")])
 def test_objectives_train(cfg, name):
@@ -74,6 +77,7 @@ def test_objectives_train(cfg, name):
 @pytest.mark.gpu
 @pytest.mark.parametrize("make,decoding", [
     (lambda m: HydraConfig(num_heads=3), None),
+    (lambda m: HydraConfig(num_heads=3, prefix_layer=True), None),
     (lambda m: RedrafterConfig(beam_width=4, beam_length=3), None),
     (lambda m: JumpConfig(target_layer=1, source_layer=1), None),
     (lambda m: DFlashConfig(block_size=4), None),
@@ -92,3 +96,30 @@ def test_lossless_on_gpu_with_graphs(cuda, make, decoding):
     out = em.decode_batch(ps, 16, decoding=dataclasses.replace(base, cuda_graphs=True))
     for a, b in zip(plain, out):
         assert torch.equal(a.tokens.cpu(), b.tokens.cpu())
+
+
+def test_hydra_prefix_layer_starts_as_identity_and_trains(model):
+    """A fresh prefix layer passes the target state through (its output projections are zero): the same heads draft
+    the same tokens with and without it. After training, its parameters have moved and decoding stays lossless."""
+    plain_heads = eco.apply(model, HydraConfig(num_heads=3))
+    with_prefix = eco.apply(model, HydraConfig(num_heads=3, prefix_layer=True))
+    with torch.no_grad():
+        for a, b in zip(plain_heads.techniques["hydra"].heads.parameters(),
+                        with_prefix.techniques["hydra"].heads.parameters()):
+            a.normal_(0, 0.02)
+            b.copy_(a)
+    dc = eco.DecodeConfig(cycle_length=4)
+    for x, y in zip(plain_heads.decode_batch(prompts(), 16, decoding=dc),
+                    with_prefix.decode_batch(prompts(), 16, decoding=dc)):
+        assert torch.equal(x.tokens, y.tokens) and x.accepted == y.accepted
+    obj = OBJECTIVES.get("step_distill")(with_prefix)
+    opt = torch.optim.Adam(obj.parameters(), lr=2e-3)
+    for _ in range(3):
+        loss, _ = obj.loss(CAL)
+        opt.zero_grad()
+        loss.backward()
+        opt.step()
+    assert with_prefix.techniques["hydra"].prefix.wo.abs().sum() > 0
+    ref = eco.apply(model).decode_batch(prompts(), 16, decoding=eco.DecodeConfig(cycle_length=1))
+    for a, b in zip(ref, with_prefix.decode_batch(prompts(), 16, decoding=dc)):
+        assert torch.equal(a.tokens, b.tokens)
