@@ -82,6 +82,10 @@ class LittleBitConfig(TechniqueConfig):
     layers: tuple[int, ...] = ()
     rank_multiple: int = 32
     backend: str = "auto"
+    qat_steps: int = 0
+    qat_lr: float = 1e-3
+    smooth_k: float = 100.0
+    calibration_tokens: int = 512
 
     def __post_init__(self) -> None:
         check_choice("method", self.method, ("dual_svid",))
@@ -90,6 +94,8 @@ class LittleBitConfig(TechniqueConfig):
         if self.backend == "triton":
             raise ConfigError("backend 'triton' is economize's Triton kernel; this build's is CUDA: use 'auto'")
         check_choice("backend", self.backend, ("auto", "reference"))
+        if self.qat_steps < 0 or self.qat_lr <= 0 or self.smooth_k <= 0 or self.calibration_tokens < 1:
+            raise ConfigError("qat_steps must be >= 0 and qat_lr, smooth_k, calibration_tokens positive")
         object.__setattr__(self, "targets", tuple(self.targets))
         object.__setattr__(self, "exclude", tuple(self.exclude))
         object.__setattr__(self, "layers", tuple(self.layers))
@@ -139,6 +145,43 @@ class LittleBitTechnique(Technique):
                         raise ConfigError(f"bpw={cfg.bpw} leaves no rank for a {out_f} x {in_f} map")
                     self.weights[key] = LittleBitWeight(*littlebit_factors(w, r, cfg.residual), m.dtype)
                 install(layer, name, self.weights[key])
+
+    def _targets(self) -> dict[int, list[str]]:
+        cfg = self.config
+        return {i: [n for n in MAPS if _selected(n, cfg.targets, cfg.exclude)] for i in self.layer_ids}
+
+    def calibrate(self, calibration) -> None:
+        """With ``qat_steps > 0``: train every selected map's factors on calibration activations (SmoothSign
+        straight-through signs, activation-aware output error; :mod:`.qat`) before the maps are replaced.
+        ``qat_report`` keeps each map's relative output error before and after."""
+        cfg = self.config
+        if cfg.qat_steps == 0:
+            return
+        from ..quant.methods import collect
+        from .qat import train_map
+
+        tokens = calibration if isinstance(calibration, (list, tuple)) else [torch.as_tensor(calibration)]
+        tokens = [t if t.dim() == 2 else t[None] for t in tokens]
+        wanted = self._targets()
+        stats = collect(self.model, tokens, wanted, False, cfg.calibration_tokens)
+        paths = 2 if cfg.residual else 1
+        self.qat_report: dict[str, tuple[float, float]] = {}
+        for i, names in wanted.items():
+            layer = self.model.layers[i]
+            for name in names:
+                w = getattr(layer, name)
+                if not isinstance(w, torch.Tensor):
+                    continue
+                out_f, in_f = w.shape
+                r = rank_for_bpw(out_f, in_f, cfg.bpw, paths=paths, multiple=cfg.rank_multiple)
+                if r == 0:
+                    continue
+                init = littlebit_factors(w, r, cfg.residual)
+                with torch.enable_grad():
+                    factors, before, after = train_map(w, stats[(i, name)].sample, init, cfg.qat_steps, cfg.qat_lr,
+                                                       cfg.smooth_k)
+                self.weights[f"{i}:{name}"] = LittleBitWeight(*factors, self.model.dtype)
+                self.qat_report[f"{i}:{name}"] = (before, after)
 
     def technique_state(self) -> dict[str, torch.Tensor]:
         out = {}

@@ -53,3 +53,25 @@ def test_sign_products_match_dense(cuda, M):
     x = torch.randn(M, 384, device=cuda).bfloat16()
     ref = x.float() @ lw.dequantize(torch.float32).t()
     torch.testing.assert_close(lw.linear(x).float(), ref, atol=0.05 * float(ref.abs().max()), rtol=0.02)
+
+
+def test_smooth_sign_gradient_and_qat_lowers_output_error():
+    from economize_b200.techniques.littlebit import LittleBitConfig
+    from economize_b200.techniques.littlebit.qat import smooth_sign
+
+    x = torch.tensor([-0.5, -0.001, 0.0, 0.001, 0.5], requires_grad=True)
+    y = smooth_sign(x, 100.0)
+    assert y.tolist() == [-1.0, -1.0, 1.0, 1.0, 1.0]
+    y.sum().backward()
+    expect = 100.0 * (1 - torch.tanh(100.0 * x.detach()) ** 2)
+    assert torch.allclose(x.grad, expect)
+    cal = torch.randint(0, 1024, (2, 48), generator=torch.Generator().manual_seed(2))
+    cfg = LittleBitConfig(bpw=1.0, layers=(1,), targets=("w_down",), rank_multiple=8, qat_steps=25, qat_lr=1e-3,
+                          calibration_tokens=96)
+    em = eco.apply(tiny_model(), cfg, calibration=cal)
+    report = em.techniques["littlebit"].qat_report
+    assert list(report) == ["0:w_down"]
+    before, after = report["0:w_down"]
+    assert after < before
+    p = prompts((17,))[0]
+    assert em.decode(p, 6, decoding=eco.DecodeConfig(cycle_length=1)).tokens.numel() == 6
