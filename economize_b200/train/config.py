@@ -32,6 +32,7 @@ class TrainConfig:
     output_dir: str | Path | None = None
     resume: bool | str | Path = False
     seed: int | None = None
+    offload_optimizer: bool = False  # AdamW master weights and moments in host memory (train/offload.py)
 
     def __post_init__(self) -> None:
         check_positive("steps", self.steps)

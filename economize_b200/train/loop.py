@@ -93,8 +93,11 @@ def fit(model, data: Any, objective: Objective | str | None = None, config: Trai
     for p in params:  # fp32 master weights while training
         p.data = p.data.float()
     d = obj.defaults
-    opt = torch.optim.AdamW(params, lr=cfg.lr or d.lr, betas=cfg.betas or d.betas,
-                            weight_decay=d.weight_decay if cfg.weight_decay is None else cfg.weight_decay)
+    opt_cls = torch.optim.AdamW
+    if cfg.offload_optimizer:
+        from .offload import OffloadedAdamW as opt_cls
+    opt = opt_cls(params, lr=cfg.lr or d.lr, betas=cfg.betas or d.betas,
+                  weight_decay=d.weight_decay if cfg.weight_decay is None else cfg.weight_decay)
     sched = make_scheduler(opt, cfg.steps, d.warmup_steps if cfg.warmup_steps is None else cfg.warmup_steps,
                            cfg.schedule or d.schedule, d.min_lr_ratio if cfg.min_lr_ratio is None else cfg.min_lr_ratio)
     clip = d.grad_clip if cfg.grad_clip is None else (cfg.grad_clip or None)

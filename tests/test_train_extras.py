@@ -113,3 +113,41 @@ def test_data_parallel_fit_keeps_ranks_in_sync():
                 p.kill()
     assert res[0][0] is True and res[1][0] is True, res
     assert res[0][1] != res[1][1]  # the ranks drew different batches
+
+
+def test_offloaded_adamw_matches_adamw():
+    import torch
+
+    from economize_b200.train.offload import OffloadedAdamW
+
+    g = torch.Generator().manual_seed(0)
+    w0 = torch.randn(8, 5, generator=g)
+    a, b = torch.nn.Parameter(w0.clone()), torch.nn.Parameter(w0.clone())
+    ref = torch.optim.AdamW([a], lr=1e-2, weight_decay=0.1)
+    off = OffloadedAdamW([b], lr=1e-2, weight_decay=0.1)
+    for step in range(5):
+        x = torch.randn(3, 8, generator=g)
+        for p, opt in ((a, ref), (b, off)):
+            opt.zero_grad()
+            (x @ p).pow(2).sum().backward()
+            opt.step()
+    assert torch.allclose(a, b, atol=1e-6)
+    state = off.state_dict()
+    again = OffloadedAdamW([torch.nn.Parameter(b.detach().clone())], lr=1e-2, weight_decay=0.1)
+    again.load_state_dict(state)
+    assert torch.equal(again._host[0], off._host[0])
+
+
+def test_fit_with_offloaded_optimizer_trains():
+    import torch
+
+    import economize_b200 as eco
+    from economize_b200.techniques.eagle3 import Eagle3Config
+    from economize_b200.train import fit
+
+    from .helpers import tiny_model
+
+    em = eco.apply(tiny_model(), Eagle3Config())
+    data = torch.randint(0, 1024, (4, 32), generator=torch.Generator().manual_seed(1))
+    res = fit(em, data, steps=4, batch_size=2, offload_optimizer=True, autocast=None, log_every=1)
+    assert res.steps == 4
