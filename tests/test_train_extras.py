@@ -151,3 +151,25 @@ def test_fit_with_offloaded_optimizer_trains():
     data = torch.randint(0, 1024, (4, 32), generator=torch.Generator().manual_seed(1))
     res = fit(em, data, steps=4, batch_size=2, offload_optimizer=True, autocast=None, log_every=1)
     assert res.steps == 4
+
+
+def test_rl_building_blocks():
+    import torch
+
+    from economize_b200.train.rl import acceptance, expected_tokens, token_log_probs
+
+    g = torch.Generator().manual_seed(0)
+    head = torch.randn(7, 5, generator=g, requires_grad=True)
+    h = torch.randn(2, 9, 5, generator=g)
+    tok = torch.randint(0, 7, (2, 9), generator=g)
+    lp, ent = token_log_probs(h, tok, lambda x: x @ head.t(), chunk=4)
+    full = torch.log_softmax(h @ head.t(), -1)
+    assert torch.allclose(lp, full.gather(-1, tok[..., None])[..., 0], atol=1e-6)
+    assert torch.allclose(ent, -(full.exp() * full).sum(-1), atol=1e-6)
+    lp.sum().backward()
+    assert head.grad is not None and head.grad.abs().sum() > 0
+    p = torch.tensor([0.5, 0.3, 0.2])
+    assert float(acceptance(p, p)) == 1.0
+    assert abs(float(acceptance(p, torch.tensor([0.0, 0.0, 1.0]))) - 0.2) < 1e-7
+    a = torch.full((4,), 0.6)
+    assert abs(float(expected_tokens(a)) - (1 - 0.6 ** 5) / (1 - 0.6)) < 1e-5
