@@ -5,7 +5,8 @@ The draft layer is EAGLE-3's (fused low/mid/high target states, its own KV cache
 the context catch-up, the anchor (the target's token after the last committed position) is the root step, and one
 more forward over ``block_size - 1`` mask tokens at the following positions, with bidirectional attention inside the
 block (every block slot's ancestor bit set), produces the remaining drafts, read out through the head. The target
-verifies (lossless). Not built: the z-lab / speculators checkpoint readers and the block training objective.
+verifies (lossless). The ``dflash_block`` objective (:mod:`.objective`) trains the root and the block drafts against
+the target's distributions. Not built: the z-lab / speculators checkpoint readers.
 """
 
 from __future__ import annotations
@@ -81,9 +82,13 @@ class DFlashDrafter(Eagle3Drafter):
 @register_technique
 class DFlashTechnique(Eagle3Technique):
     config_class = DFlashConfig
+    objective_name = "dflash_block"
 
     def drafter(self) -> DFlashDrafter:
         return DFlashDrafter(self)
 
     def default_decoding(self) -> DecodeConfig:
         return DecodeConfig(cycle_length=self.config.block_size)
+
+
+from . import objective as _objective  # noqa: E402,F401  (registers the dflash_block objective)

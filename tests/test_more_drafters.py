@@ -123,3 +123,22 @@ def test_hydra_prefix_layer_starts_as_identity_and_trains(model):
     ref = eco.apply(model).decode_batch(prompts(), 16, decoding=eco.DecodeConfig(cycle_length=1))
     for a, b in zip(ref, with_prefix.decode_batch(prompts(), 16, decoding=dc)):
         assert torch.equal(a.tokens, b.tokens)
+
+
+def test_dflash_block_objective_trains():
+    em = eco.apply(tiny_model(), DFlashConfig(block_size=4))
+    obj = OBJECTIVES.get("dflash_block")(em, anchors=8)
+    opt = torch.optim.Adam(obj.parameters(), lr=3e-3)
+    data = torch.randint(0, 1024, (2, 24), generator=torch.Generator().manual_seed(5))
+    losses = []
+    for _ in range(8):
+        loss, metrics = obj.loss(data)
+        opt.zero_grad()
+        loss.backward()
+        opt.step()
+        losses.append(float(loss.detach()))
+    assert {"root_kl", "block_kl", "block_acc"} <= set(metrics)
+    assert min(losses[1:]) < losses[0], losses
+    ref = eco.apply(tiny_model()).decode_batch(prompts(), 12, decoding=eco.DecodeConfig(cycle_length=1))
+    for a, b in zip(ref, em.decode_batch(prompts(), 12)):
+        assert torch.equal(a.tokens, b.tokens)
