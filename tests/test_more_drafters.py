@@ -142,3 +142,30 @@ def test_dflash_block_objective_trains():
     ref = eco.apply(tiny_model()).decode_batch(prompts(), 12, decoding=eco.DecodeConfig(cycle_length=1))
     for a, b in zip(ref, em.decode_batch(prompts(), 12)):
         assert torch.equal(a.tokens, b.tokens)
+
+
+def test_dflash_block_objective_matches_the_drafter():
+    """The objective's root and block logits for an anchor equal what the drafter computes at inference after a
+    prefill of the same context (same layer, same masks)."""
+    from economize_b200.runtime.cache import StepBatch
+    from economize_b200.techniques.dflash.objective import block_logits
+
+    em = eco.apply(tiny_model(), DFlashConfig(block_size=4))
+    tech = em.techniques["dflash"]
+    tech.reset_parameters(seed=7)
+    model = em.model
+    prompt = prompts((17,))[0]
+    tokens = torch.cat([prompt, torch.tensor([123])])  # the context and the anchor (the root token)
+    n = tokens.numel()
+    with torch.no_grad():
+        _, aux = model.forward_step(tokens[None], StepBatch.prefill(torch.tensor([n], dtype=torch.int32), n),
+                                    model.new_cache(1, 128), tech.aux_layers)
+        d = tech.drafter()
+        d.begin(1, 128)
+        fused = d.fuse(aux)[:, :-1]  # the features of the context tokens (the anchor's own are not used)
+        sources = torch.cat([torch.zeros_like(fused[:, :1]), fused], 1)
+        root_logits, _ = d.observe(tokens[None], sources, torch.zeros(1, dtype=torch.int32),
+                                   torch.tensor([n], dtype=torch.int32), torch.tensor([n - 1]))
+        root, block = block_logits(tech, aux, tokens[None], torch.tensor([n - 1]), d.mask_id)
+    torch.testing.assert_close(root[0, 0], root_logits[0], atol=2e-4, rtol=2e-4)
+    torch.testing.assert_close(block[0, 0], d.stash[0], atol=2e-4, rtol=2e-4)
