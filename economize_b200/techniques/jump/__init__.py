@@ -32,7 +32,9 @@ __all__ = ["JumpConfig", "JumpDrafter", "JumpPredictor", "JumpTechnique"]
 @dataclass(frozen=True)
 class JumpConfig(TechniqueConfig):
     """``target_layer`` ``m`` and ``source_layer`` ``u`` (1-indexed, ``m <= u``); ``exit_layer`` ``r`` (``None``:
-    the last layer); ``predictor``: ``"mlp"``; ``width``: the predictor's inner width multiple of the hidden size."""
+    the last layer); ``predictor``: ``"mlp"``; ``width``: the predictor's inner width multiple of the hidden size;
+    ``source_layers``: several sources in ``m .. r`` combined by ``mixer`` (``"concat"``, ``"linear"``,
+    ``"attention"``) instead of the one ``source_layer``."""
 
     technique: ClassVar[str] = "jump"
     target_layer: int | None = None
@@ -41,9 +43,13 @@ class JumpConfig(TechniqueConfig):
     predictor: str = "mlp"
     width: float = 1.0
     param_dtype: str = "float32"
+    source_layers: tuple[int, ...] = ()
+    mixer: str = "concat"
 
     def __post_init__(self) -> None:
         check_choice("predictor", self.predictor, ("mlp",))
+        check_choice("mixer", self.mixer, MIXERS)
+        object.__setattr__(self, "source_layers", tuple(sorted({int(u) for u in self.source_layers})))
         check_positive("width", self.width)
         check_choice("param_dtype", self.param_dtype, ("float32", "model"))
 
@@ -53,12 +59,58 @@ class JumpConfig(TechniqueConfig):
         r = self.exit_layer or num_layers
         return m, u, r
 
+    def sources(self, num_layers: int) -> tuple[int, ...]:
+        """The source layers (``source_layers``, else the one ``source_layer``)."""
+        return self.source_layers or (self.resolved(num_layers)[1],)
+
     def validate(self, model) -> None:
         n = model.config.num_layers
         m, u, r = self.resolved(n)
         if not 1 <= m <= u <= r <= n or m >= r:
             raise ConfigError(f"jump needs 1 <= target_layer <= source_layer <= exit_layer <= {n} and "
                               f"target_layer < exit_layer, got {(m, u, r)}")
+        if any(not m <= v <= r for v in self.sources(n)):
+            raise ConfigError(f"source_layers must lie in target_layer .. exit_layer ({m} .. {r}): the drafter's "
+                              f"partial pass produces only those states, got {self.sources(n)}")
+
+
+#: source mixers (several source layers -> one predictor source; economize ``techniques/jump/mixer.py``):
+#: ``concat``: a linear map of the concatenated states (starts as the last source); ``linear``: a learned convex
+#: combination of the states (starts on the last); ``attention``: per-token softmax weights from a learned query
+#: against the RMS-normalized states.
+MIXERS = ("concat", "linear", "attention")
+
+
+class SourceMixer(nn.Module):
+    def __init__(self, kind: str, n: int, hidden: int) -> None:
+        super().__init__()
+        self.kind, self.n = kind, n
+        if kind == "concat" and n > 1:
+            self.proj = nn.Linear(n * hidden, hidden, bias=False)
+            with torch.no_grad():
+                self.proj.weight.zero_()
+                self.proj.weight[:, (n - 1) * hidden:].copy_(torch.eye(hidden))
+        elif kind == "linear":
+            init = torch.full((n,), -8.0)
+            init[-1] = 8.0
+            self.logits = nn.Parameter(init)
+        elif kind == "attention":
+            self.query = nn.Parameter(torch.zeros(hidden))
+
+    def forward(self, states: torch.Tensor) -> torch.Tensor:
+        """``states [..., n, H]`` (ascending layers) -> ``[..., H]``."""
+        if self.n == 1:
+            return states[..., 0, :]
+        x = states.float()
+        if self.kind == "concat":
+            return self.proj(x.flatten(-2).to(self.proj.weight.dtype))
+        if self.kind == "linear":
+            w = torch.softmax(self.logits.float(), 0)
+        else:
+            normed = x * torch.rsqrt(x.pow(2).mean(-1, keepdim=True) + 1e-6)
+            w = torch.softmax((normed * self.query.float()).sum(-1), -1)[..., None]
+            return (w * x).sum(-2)
+        return (w[:, None] * x).sum(-2)
 
 
 class JumpPredictor(nn.Module):
@@ -81,7 +133,7 @@ class JumpDrafter:
     def __init__(self, tech: JumpTechnique) -> None:
         self.tech = tech
         self.m, self.u, self.r = tech.layers
-        self.capture_layers = (self.u,)
+        self.capture_layers = tech.sources
         self.carry_size = tech.model.config.hidden_size
         self.cache = None
 
@@ -92,16 +144,16 @@ class JumpDrafter:
         self.cache = cache
 
     def fuse(self, aux):
-        return aux[self.u]
+        return self.tech.mix(aux).to(self.tech.model.dtype)
 
     def _run(self, tokens, states, batch: StepBatch):
         tech = self.tech
         model = tech.model
         h_m = tech.predictor(states, model.embed_tokens(tokens.clamp_min(0))).to(model.dtype)
-        cap = (-2,) if self.u == self.r else (self.u,)
+        cap = tuple(-2 if v == self.r else v for v in tech.sources)  # the last run layer's output is -2
         out, aux = model.forward_step(tokens.clamp_min(0), batch, self.cache, capture=cap,
                                       layers=range(self.m, self.r), hidden=h_m)
-        nxt = aux[cap[0]]
+        nxt = tech.mix(aux, cap).to(model.dtype)
         return model.logits(out).float(), nxt
 
     def observe(self, tokens, sources, kv_len, n_valid, root):
@@ -138,6 +190,14 @@ class JumpTechnique(Technique):
         self.layers = config.resolved(model.config.num_layers)
         dtype = torch.float32 if config.param_dtype == "float32" else model.dtype
         self.predictor = JumpPredictor(h, max(8, int(config.width * h))).to(device=model.device, dtype=dtype)
+        self.sources = config.sources(model.config.num_layers)
+        self.mixer = SourceMixer(config.mixer, len(self.sources), h).to(device=model.device, dtype=dtype)
+
+    def mix(self, aux: dict[int, torch.Tensor], keys: tuple[int, ...] | None = None) -> torch.Tensor:
+        """The predictor's source from captured states ``aux`` (``keys``: their capture indices, default the
+        source layers)."""
+        keys = keys or self.sources
+        return self.mixer(torch.stack([aux[k] for k in keys], -2))
 
     def drafter(self):
         return JumpDrafter(self)
@@ -160,7 +220,7 @@ class JumpRollout(Objective):
         self.tech = model.techniques["jump"]
 
     def parameters(self):
-        return list(self.tech.predictor.parameters())
+        return list(self.tech.predictor.parameters()) + list(self.tech.mixer.parameters())
 
     def loss(self, tokens: torch.Tensor):
         tech = self.tech
@@ -170,9 +230,9 @@ class JumpRollout(Objective):
         with torch.no_grad():
             cache = model.new_cache(b, ((s + 127) // 128) * 128)
             lengths = torch.full((b,), s, dtype=torch.int32, device=tokens.device)
-            _, aux = model.forward_step(tokens, StepBatch.prefill(lengths, s), cache, capture=(m, u))
+            _, aux = model.forward_step(tokens, StepBatch.prefill(lengths, s), cache, capture=(m, *tech.sources))
             emb = model.embed_tokens(tokens)
-        pred = tech.predictor(aux[u][:, :-1].float(), emb[:, 1:].float())
+        pred = tech.predictor(tech.mix(aux)[:, :-1].float(), emb[:, 1:].float())
         target = aux[m][:, 1:].float()
         err = (pred.float() - target).pow(2).sum(-1) / target.pow(2).sum(-1).clamp_min(1e-6)
         loss = err.mean()

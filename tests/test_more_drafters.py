@@ -38,6 +38,9 @@ def plain(model):
     (lambda: RedrafterConfig(beam_length=4), eco.DecodeConfig(cycle_length=4)),
     (lambda: PardConfig(model=tiny_model(num_layers=2, seed=1), max_drafts=4), None),
     (lambda: JumpConfig(target_layer=1, source_layer=2), None),
+    (lambda: JumpConfig(target_layer=1, source_layers=(2, 3), mixer="concat"), None),
+    (lambda: JumpConfig(target_layer=1, source_layers=(1, 4), mixer="attention"), TREE),
+    (lambda: JumpConfig(target_layer=2, source_layers=(2, 3, 4), mixer="linear"), None),
     (lambda: JumpConfig(target_layer=1, source_layer=3, exit_layer=3), TREE),
     (lambda: DFlashConfig(block_size=5), None),
     (lambda: DFlashConfig(block_size=5), TREE),
@@ -59,7 +62,9 @@ def test_pard_self_draft_accepts(model, plain):
 @pytest.mark.parametrize("cfg,name", [(HydraConfig(num_heads=3), "step_distill"),
                                       (HydraConfig(num_heads=3, prefix_layer=True), "step_distill"),
                                       (RedrafterConfig(beam_length=3), "step_distill"),
-                                      (JumpConfig(target_layer=1, source_layer=2), "jump_rollout")])
+                                      (JumpConfig(target_layer=1, source_layer=2), "jump_rollout"),
+                                      (JumpConfig(target_layer=1, source_layers=(2, 3), mixer="attention"),
+                                       "jump_rollout")])
 def test_objectives_train(cfg, name):
     em = eco.apply(tiny_model(), cfg)
     obj = OBJECTIVES.get(name)(em)
@@ -169,3 +174,18 @@ def test_dflash_block_objective_matches_the_drafter():
         root, block = block_logits(tech, aux, tokens[None], torch.tensor([n - 1]), d.mask_id)
     torch.testing.assert_close(root[0, 0], root_logits[0], atol=2e-4, rtol=2e-4)
     torch.testing.assert_close(block[0, 0], d.stash[0], atol=2e-4, rtol=2e-4)
+
+
+def test_jump_mixers_start_on_the_last_source():
+    from economize_b200.techniques.jump import JumpConfig as JC
+
+    model = tiny_model()
+    one = eco.apply(model, JC(target_layer=1, source_layer=3))
+    for mixer in ("concat", "linear"):
+        many = eco.apply(tiny_model(), JC(target_layer=1, source_layers=(2, 3), mixer=mixer))
+        many.techniques["jump"].predictor.load_state_dict(one.techniques["jump"].predictor.state_dict())
+        dc = eco.DecodeConfig(cycle_length=4)
+        for a, b in zip(one.decode_batch(prompts(), 12, decoding=dc), many.decode_batch(prompts(), 12, decoding=dc)):
+            assert torch.equal(a.tokens, b.tokens) and a.accepted == b.accepted
+    with pytest.raises(eco.ConfigError, match="source_layers"):
+        eco.apply(tiny_model(), JC(target_layer=2, source_layers=(1, 3)))
