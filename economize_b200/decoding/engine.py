@@ -409,7 +409,7 @@ class SpecEngine:
         rows = torch.arange(batch, device=dev)
         if not getattr(drafter, "observes", True):
             st.last.copy_(out[rows, n_acc.long()])
-            st.kv_len.add_(n_acc + 1)
+            st.kv_len.add_(torch.where(active, n_acc + 1, 0).to(st.kv_len.dtype))  # finished rows stay
             st.n_out.add_(n_acc + 1)
             return
         # ---- observe: drafter state for the committed columns + next root step ----
@@ -423,7 +423,7 @@ class SpecEngine:
             root_logits, root_state = drafter.observe(obs_tokens, sources, st.kv_len, n_valid, n_valid - 1)
         st.carry.copy_(fused[rows, n_acc.long()])
         st.last.copy_(out[rows, n_acc.long()])
-        st.kv_len.add_(n_acc + 1)
+        st.kv_len.add_(torch.where(active, n_acc + 1, 0).to(st.kv_len.dtype))  # finished rows stay
         st.n_out.add_(n_acc + 1)
         if root_logits is not None:
             st.root_logits.copy_(root_logits)
