@@ -27,7 +27,7 @@ def main(argv: list[str] | None = None) -> None:
     from economize_b200.techniques.eagle3 import Eagle3Config
 
     p = argparse.ArgumentParser(description=__doc__.splitlines()[0])
-    p.add_argument("--mode", choices=["tree", "chain", "plain"], default="tree")
+    p.add_argument("--mode", choices=["tree", "chain", "plain", "sequoia", "specexec"], default="tree")
     p.add_argument("--batch", type=int, default=1)
     p.add_argument("--prompt-len", type=int, default=512)
     p.add_argument("--new-tokens", type=int, default=64)
@@ -45,6 +45,13 @@ def main(argv: list[str] | None = None) -> None:
     if a.mode == "tree":
         dc = eco.DecodeConfig(cycle_length=7, draft_policy="dynamic_tree", cuda_graphs=True,
                               draft_policy_options={"depth": 6, "topk": 10, "total_tokens": 60})
+    elif a.mode == "sequoia":  # a static tree of 60 nodes shaped for typical EAGLE acceptance rates
+        dc = eco.DecodeConfig(cycle_length=7, draft_policy="sequoia", cuda_graphs=True,
+                              draft_policy_options={"acceptance": (0.6, 0.15, 0.06, 0.03), "total_tokens": 60,
+                                                    "depth": 6})
+    elif a.mode == "specexec":
+        dc = eco.DecodeConfig(cycle_length=7, draft_policy="specexec", cuda_graphs=True,
+                              draft_policy_options={"depth": 6, "width": 10, "topk": 10, "total_tokens": 60})
     elif a.mode == "chain":
         dc = eco.DecodeConfig(cycle_length=7, cuda_graphs=True)
     else:
