@@ -101,3 +101,15 @@ def test_generate_hf_style(em):
     ids = torch.stack([prompts((12,))[0]])
     out = em.generate(ids, max_new_tokens=8, decoding=eco.DecodeConfig(cycle_length=3))
     assert out.shape == (1, 20) and torch.equal(out[0, :12], ids[0])
+
+
+def test_finished_rows_stop_advancing(em):
+    """A row that reached its token budget keeps its KV position while the other rows decode on (its cache never
+    runs past the capacity reserved for it)."""
+    cfg = eco.DecodeConfig(cycle_length=7, draft_policy="dynamic_tree", draft_policy_options=TREE)
+    ps = prompts()
+    out = em.decode_batch(ps, [2, 30], decoding=cfg)
+    assert [r.tokens.numel() for r in out] == [2, 30]
+    engine = em.decoder(cfg)
+    (state,) = engine._states.values()
+    assert int(state.kv_len[0]) <= ps[0].numel() + 1 + 7  # prefill token + at most one cycle's commit
