@@ -111,5 +111,5 @@ def test_finished_rows_stop_advancing(em):
     out = em.decode_batch(ps, [2, 30], decoding=cfg)
     assert [r.tokens.numel() for r in out] == [2, 30]
     engine = em.decoder(cfg)
-    (state,) = engine._states.values()
+    state = next(s for (b, _, out_cap), s in engine._states.items() if b == 2 and out_cap == 30 + engine.depth + 2)
     assert int(state.kv_len[0]) <= ps[0].numel() + 1 + 7  # prefill token + at most one cycle's commit
