@@ -1,24 +1,27 @@
 """Headline benchmark: decode tokens/s + mean accepted length, Llama-3.1-8B + EAGLE-3 dynamic tree on B200.
 
-    python bench.py [--gpus N] [--steps K] [--warmup W] [--batch B] [--impl ours|reference]
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--batch B] [--impl ours|reference] [--parallel tp|dp]
 
 One *step* generates ``--new-tokens`` (256) tokens after uniform-random prompts of ``--prompt-len`` (512) tokens for
-``--batch`` rows per GPU through the public API (``EfficientModel.decode_batch``), prefill included. The target is a
-random-init Llama-3.1-8B architecture (bf16, seed 0) and the drafter an EAGLE-3 head (draft vocabulary 32000)
-trained briefly on the target's own greedy continuations of synthetic prompts (``--train-steps``; 0 keeps the
-random head). Decoding: dynamic tree, depth 6, top-k 10, 60 nodes, CUDA graphs.
+``--batch`` rows through the public API (``decode_batch``), prefill included. The target is a random-init
+Llama-3.1-8B architecture (bf16, N(0, 0.02), seed 0) and the drafter an EAGLE-3 head (draft vocabulary 32000).
+Decoding: dynamic tree, depth 6, top-k 10, 60 nodes, CUDA graphs.
 
-With N > 1 GPUs (launched by torchrun) every rank serves its own batch (data-parallel replicas; ``scaling``
-"weak"); the step time is the max over ranks of the CUDA-event time. ``value`` is the whole job's generated tokens
-per second. The model weights (16 GB) exceed L2, so every step streams them from HBM (no flush needed).
+Both arms build the same target weights and the same drafter initialisation with the plain PyTorch code of this
+file, then each trains its drafter with its OWN ``train.fit`` on its OWN target's greedy continuations of the
+benchmark prompts (the same recipe: steps, rounds, batch, learning rate), so neither arm runs the other's code.
+``--impl reference`` imports only the unmodified reference (``baseline/_ref``) and ``transformers``.
 
-``--impl reference`` runs the same metric through the unmodified reference (``baseline/_ref``: economize on
-Hugging Face transformers) with the same target and drafter weights.
+With N > 1 GPUs (launched by torchrun) the default is tensor parallelism: one request stream served by all ranks
+(``scaling`` "strong"); ``--parallel dp`` runs one replica per GPU instead ("weak"). The step time is the max over
+ranks of the CUDA-event time; ``value`` is the whole job's generated tokens per second. The model weights (16 GB)
+exceed L2, so every step streams them from HBM (no flush needed).
 """
 
 from __future__ import annotations
 
 import argparse
+import glob
 import json
 import os
 import statistics
@@ -33,6 +36,7 @@ HERE = os.path.dirname(os.path.abspath(__file__))
 METRIC = "decode tok/s + mean accepted len, Llama-3.1-8B EAGLE-3 tree, 1/2/4/8 B200"
 BASELINE_TOKS = None  # BASELINE.md publishes no B200 number for this config
 TREE = {"depth": 6, "topk": 10, "total_tokens": 60}
+DRAFT_VOCAB = 32000
 
 
 def parse() -> argparse.Namespace:
@@ -43,16 +47,20 @@ def parse() -> argparse.Namespace:
     p.add_argument("--batch", type=int, default=1)
     p.add_argument("--prompt-len", type=int, default=512)
     p.add_argument("--new-tokens", type=int, default=256)
-    p.add_argument("--train-steps", type=int, default=150)
+    p.add_argument("--train-steps", type=int, default=600)
     p.add_argument("--train-rounds", type=int, default=3)
     p.add_argument("--impl", choices=("ours", "reference"), default="ours")
     p.add_argument("--model", choices=("llama31_8b", "tiny"), default="llama31_8b")
     p.add_argument("--no-graphs", action="store_true")
-    p.add_argument("--parallel", choices=("dp", "tp"), default="dp",
-                   help="dp: one replica per GPU; tp: one model sharded over all GPUs (fused NVLink collectives)")
-    p.add_argument("--nccl-tp", action="store_true", help="with --parallel tp: NCCL all-reduces instead of the fused "
-                   "GEMM->push / reduce+RMSNorm kernels")
-    return p.parse_args()
+    p.add_argument("--parallel", choices=("dp", "tp"), default=None,
+                   help="dp: one replica per GPU; tp: one model sharded over all GPUs (default with N > 1)")
+    p.add_argument("--nccl-tp", action="store_true", help="with tp: NCCL all-reduces instead of the fused kernels")
+    p.add_argument("--attn", default=None, help="reference arm: attention implementation (default: economize's "
+                   "own kernel, falling back to sdpa, then eager, if it cannot run)")
+    args = p.parse_args()
+    if args.parallel is None:
+        args.parallel = "tp" if int(os.environ.get("WORLD_SIZE", "1")) > 1 else "dp"
+    return args
 
 
 class ClockSampler:
@@ -98,7 +106,9 @@ class ClockSampler:
                 "reasons": reasons, "samples": len(sm)}
 
 
-def setup_dist(args: argparse.Namespace):
+# ---- process group ---------------------------------------------------------------------------------------------
+
+def setup_dist():
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
     local = int(os.environ.get("LOCAL_RANK", "0"))
@@ -108,7 +118,7 @@ def setup_dist(args: argparse.Namespace):
 
         import torch.distributed as dist
 
-        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=1800),
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=900),
                                 device_id=torch.device("cuda", local))
     return world, rank, local
 
@@ -140,151 +150,377 @@ def barrier(world: int) -> None:
         dist.barrier()
 
 
-def build_target(args):
-    from economize_b200.models.config import llama31_8b, tiny_llama
-    from economize_b200.models.llama import CausalLM, init_weights
+# ---- shared by both arms: plain PyTorch + transformers only ------------------------------------------------------
 
-    cfg = llama31_8b() if args.model == "llama31_8b" else tiny_llama(head_dim=128, num_heads=2, num_kv_heads=1)
-    return init_weights(CausalLM(cfg, torch.bfloat16, "cuda"), seed=0)
+def hf_config(model: str):
+    """The ``transformers`` config of the benchmark architecture."""
+    import transformers
+
+    if model == "tiny":
+        return transformers.LlamaConfig(vocab_size=1024, hidden_size=256, intermediate_size=688, num_hidden_layers=4,
+                                        num_attention_heads=2, num_key_value_heads=1, head_dim=128,
+                                        rms_norm_eps=1e-5, rope_theta=1e4, max_position_embeddings=4096,
+                                        tie_word_embeddings=False)
+    return transformers.LlamaConfig(
+        vocab_size=128256, hidden_size=4096, intermediate_size=14336, num_hidden_layers=32, num_attention_heads=32,
+        num_key_value_heads=8, head_dim=128, rms_norm_eps=1e-5, rope_theta=500000.0,
+        rope_scaling={"rope_type": "llama3", "factor": 8.0, "low_freq_factor": 1.0, "high_freq_factor": 4.0,
+                      "original_max_position_embeddings": 8192},
+        max_position_embeddings=131072, tie_word_embeddings=False)
+
+
+@torch.no_grad()
+def build_hf_target(model: str, attn: str = "sdpa"):
+    """A ``transformers`` Llama on the GPU with the benchmark weights: every matrix N(0, 0.02) drawn in bf16-rounded
+    fp32 from one CUDA generator (seed 0) in state-dict name order, norms at one."""
+    import transformers
+
+    cfg = hf_config(model)
+    cfg._attn_implementation = attn
+    with torch.device("meta"):
+        hf = transformers.LlamaForCausalLM(cfg)
+    hf = hf.to_empty(device="cuda").to(torch.bfloat16)
+    gen = torch.Generator(device="cuda")
+    gen.manual_seed(0)
+    for name, p in sorted(hf.named_parameters()):
+        if p.dim() >= 2:
+            p.copy_(torch.randn(p.shape, generator=gen, device="cuda", dtype=torch.float32).mul_(0.02))
+        else:
+            p.fill_(1.0)
+    # the rotary inverse frequencies (non-persistent buffers, left empty by the meta construction): recomputed in
+    # fp32 exactly as the module's constructor does
+    emb = hf.model.rotary_emb
+    fresh = type(emb)(emb.config, device="cuda")
+    emb.register_buffer("inv_freq", fresh.inv_freq, persistent=False)
+    emb.register_buffer("original_inv_freq", fresh.original_inv_freq, persistent=False)
+    emb.attention_scaling = fresh.attention_scaling
+    return hf.eval()
+
+
+def prompts_for(args, stream: int, vocab: int) -> torch.Tensor:
+    g = torch.Generator().manual_seed(1234 + stream)
+    return torch.randint(0, vocab, (args.batch, args.prompt_len), generator=g).to("cuda")
+
+
+def draft_vocab_ids(tokens: torch.Tensor, vocab: int, k: int) -> torch.Tensor:
+    """EAGLE-3's draft vocabulary: the ``k`` most frequent ids of ``tokens`` (ties and unseen ids in id order),
+    returned in ascending id order."""
+    counts = torch.bincount(tokens.reshape(-1).long().cpu(), minlength=vocab)[:vocab].double()
+    order = torch.argsort(-counts * vocab + torch.arange(vocab, dtype=torch.float64), stable=True)
+    return order[:k].sort().values
+
+
+@torch.no_grad()
+def eagle3_init_state(shapes: dict[str, tuple], lm_head: torch.Tensor, ids: torch.Tensor) -> dict[str, torch.Tensor]:
+    """The drafter's starting weights in economize's EAGLE-3 parameter names: an early exit of the target (``fc``
+    selects the highest fused feature, the attention and MLP output maps are zero, the head is the target's head
+    restricted to the draft vocabulary), the other matrices N(0, 0.02) from a CUDA generator (seed 1)."""
+    gen = torch.Generator(device="cuda")
+    gen.manual_seed(1)
+    out: dict[str, torch.Tensor] = {}
+    for name in sorted(shapes):
+        shape = shapes[name]
+        if name == "d2t":
+            out[name] = (ids.to("cuda") - torch.arange(ids.numel(), device="cuda")).to(torch.int64)
+        elif name == "t2d":
+            t2d = torch.zeros(shape, dtype=torch.bool, device="cuda")
+            t2d[ids.to("cuda")] = True
+            out[name] = t2d
+        elif name == "fc.weight":
+            h = shape[0]
+            fc = torch.zeros(shape, dtype=torch.bfloat16, device="cuda")
+            fc[:, -h:] = torch.eye(h, dtype=torch.bfloat16, device="cuda")
+            out[name] = fc
+        elif name == "lm_head.weight":
+            out[name] = lm_head[ids.to(lm_head.device)].to(torch.bfloat16).contiguous()
+        elif len(shape) >= 2:
+            w = torch.randn(shape, generator=gen, device="cuda", dtype=torch.float32).mul_(0.02)
+            if name.endswith(("o_proj.weight", "down_proj.weight")):
+                w.zero_()
+            out[name] = w.to(torch.bfloat16)
+        elif name.endswith(".bias"):
+            out[name] = torch.zeros(shape, dtype=torch.bfloat16, device="cuda")
+        else:
+            out[name] = torch.ones(shape, dtype=torch.bfloat16, device="cuda")
+    return out
+
+
+def with_prompts(prompts, results) -> torch.Tensor:
+    return torch.stack([torch.cat([p, r.tokens.to(p.device)]) for p, r in zip(prompts, results)])
 
 
 CACHE_DIR = os.environ.get("ECZ_BENCH_CACHE", "/tmp/economize_b200_bench")
 
 
-def _cache_path(args, rank: int, world: int) -> str:
-    key = (f"{args.model}-b{args.batch}-p{args.prompt_len}-n{args.new_tokens}-t{args.train_steps}x{args.train_rounds}"
-           f"-r{rank}-w{world}-v4")
+def _cache_path(args, impl: str, stream: int) -> str:
+    key = (f"{impl}-{args.model}-b{args.batch}-p{args.prompt_len}-n{args.new_tokens}-t{args.train_steps}"
+           f"x{args.train_rounds}-s{stream}-v5")
     return os.path.join(CACHE_DIR, f"drafter-{key}.pt")
 
 
-def reference_module():
-    """The installed reference package (``baseline/_ref``), or ``None``."""
-    ref_dir = os.path.join(HERE, "baseline", "_ref")
-    if not os.path.isdir(os.path.join(ref_dir, "economize")):
-        return None
-    if ref_dir not in sys.path:
-        sys.path.insert(0, ref_dir)
-    try:
-        import economize
-
-        return economize
-    except Exception:
-        return None
-
-
-def hf_twin(target):
-    """A ``transformers`` Llama with the target's weights (bf16, on the GPU)."""
-    import transformers
-
-    hcfg = target.config.to_hf()
-    with torch.device("cuda"):
-        hf = transformers.LlamaForCausalLM(hcfg).to(torch.bfloat16).eval()
-    hf.load_state_dict(target.hf_state_dict())
-    return hf
-
-
-def plain_continuations_ref(ref, hf, prompts, new_tokens):
-    model = ref.apply(hf)
-    out = model.decode_batch(list(prompts), new_tokens, decoding=ref.DecodeConfig(cycle_length=1))
-    rows = torch.stack([torch.cat([p, r.tokens.to(p.device)]) for p, r in zip(prompts, out)])
-    model.detach()
-    return rows
-
-
-def build_drafter(target, args, rank: int, world: int, prompts, hf=None):
-    """EAGLE-3 head weights shared by both arms, in the reference's parameter names.
-
-    The random-init target's greedy continuation is chaotic, so a drafter can only be accurate where it has seen
-    the continuation: it is trained (``--train-steps``) on the plain greedy continuations of the benchmark prompts
-    produced by BOTH implementations (each arm's own bf16 rounding leads to its own trajectory), starting from an
-    early-exit initialisation (fc picks the highest feature, the layer passes it through, the head is the target's
-    restricted to the 32000 most frequent continuation tokens). The result is cached on the box, so the arm that
-    runs second loads exactly the weights the first one trained.
-    """
-    import economize_b200 as eco
-    from economize_b200.techniques.eagle3 import Eagle3Config
-    from economize_b200.techniques.eagle3.formats import from_reference_state, to_reference_state
-
-    vocab = min(32000, target.config.vocab_size)
-    em = eco.apply(target, Eagle3Config(draft_vocab=vocab))
-    tech = em.techniques["eagle3"]
-    path = _cache_path(args, rank, world)
+def train_drafter(arm, args, prompts, path: str, log) -> None:
+    """The drafter recipe, identical for both arms: the draft vocabulary from the arm's own plain greedy
+    continuations, the early-exit initialisation, then ``--train-rounds`` rounds of the arm's own ``fit``, each
+    round adding the speculative trajectories the current drafter produces (a tree pass may round differently from
+    a one-token pass, so a speculative trajectory can leave the plain one). Cached on the box per arm."""
     if os.path.exists(path):
-        from_reference_state(tech, torch.load(path, map_location="cuda", weights_only=True))
-        return em, to_reference_state(tech)
-    tech.reset_parameters(seed=1, identity=True)
-    if args.train_steps > 0:
-        from economize_b200.train import fit
-
-        def with_prompts(results):
-            return torch.stack([torch.cat([p, r.tokens.to(p.device)]) for p, r in zip(prompts, results)])
-
-        plain = em.decode_batch(list(prompts), args.new_tokens,
-                                decoding=eco.DecodeConfig(cycle_length=1, cuda_graphs=True))
-        data = with_prompts(plain)
-        ref = reference_module()
-        ref_model = None
-        own_hf = False
-        if ref is not None:
-            own_hf = hf is None
-            hf = hf if hf is not None else hf_twin(target)
-            try:
-                from economize.techniques.eagle3 import Eagle3Config as RefEagle3Config
-
-                ref_model = ref.apply(hf, RefEagle3Config(draft_vocab=vocab, param_dtype="model"))
-                ref_cfg = ref.DecodeConfig(cycle_length=TREE["depth"] + 1, draft_policy="dynamic_tree",
-                                           draft_policy_options=dict(TREE), cuda_graphs=True)
-            except Exception as err:
-                print(f"[bench] reference drafter unavailable for training rows ({err})", file=sys.stderr)
-
-        def ref_trajectories():
-            ref_tech = ref_model.techniques["eagle3"]
-            cur = ref_tech.state_dict()
-            ref_tech.load_state_dict({k: v.to(cur[k].device, cur[k].dtype)
-                                      for k, v in to_reference_state(tech).items()})
-            return with_prompts(ref_model.decode_batch(list(prompts), args.new_tokens, decoding=ref_cfg))
-
-        tech.draft_vocab_from(data[:, args.prompt_len:])
-        if ref_model is not None:  # the reference's own greedy trajectory (its tree path, untrained drafter)
-            data = torch.cat([data, ref_trajectories()])
-            tech.extend_draft_vocab(data[:, args.prompt_len:], data[:1, args.prompt_len:])
-        # bf16 tree verification rounds differently from one-token passes and the random target is chaotic, so
-        # every implementation's speculative trajectory drifts from its plain one; each round adds the
-        # trajectories the current drafter produces in both implementations.
-        rounds = max(1, args.train_rounds)
-        for rnd in range(rounds):
-            fit(em, data, steps=max(1, args.train_steps // rounds), batch_size=min(4, data.shape[0]), seed=rnd,
-                lr=1e-3, warmup_steps=5, log_every=max(1, args.train_steps))
-            if rnd + 1 < rounds:
-                seen = data[:, args.prompt_len:]
-                new = [with_prompts(em.decode_batch(list(prompts), args.new_tokens, decoding=decode_config(args)))]
-                if ref_model is not None:
-                    new.append(ref_trajectories())
-                data = torch.cat([data, *new])
-                tech.extend_draft_vocab(data[:, args.prompt_len:], seen)
-        if ref_model is not None:
-            ref_model.detach()
-        if own_hf:
-            del hf
-            torch.cuda.empty_cache()
-    state = to_reference_state(tech)
+        arm.load_state(torch.load(path, map_location="cuda", weights_only=True))
+        log(f"drafter loaded from {path}")
+        return
+    t0 = time.perf_counter()
+    data = with_prompts(prompts, arm.decode(prompts, plain=True))
+    ids = draft_vocab_ids(data[:, args.prompt_len:], arm.vocab, min(DRAFT_VOCAB, arm.vocab))
+    arm.load_state(eagle3_init_state(arm.state_shapes(), arm.lm_head(), ids))
+    rounds = max(1, args.train_rounds)
+    for rnd in range(rounds if args.train_steps > 0 else 0):
+        arm.fit(data, steps=max(1, args.train_steps // rounds), seed=rnd)
+        if rnd + 1 < rounds:
+            spec = with_prompts(prompts, arm.decode(prompts, plain=False))
+            fresh = [row for row in spec if not any(torch.equal(row, old) for old in data)]
+            if fresh:
+                data = torch.cat([data, torch.stack(fresh)])
+    state = {k: v.detach().cpu() for k, v in arm.state().items()}
     os.makedirs(CACHE_DIR, exist_ok=True)
     tmp = path + f".{os.getpid()}.tmp"
-    torch.save({k: v.cpu() for k, v in state.items()}, tmp)
+    torch.save(state, tmp)
     os.replace(tmp, path)
-    return em, state
+    log(f"drafter trained: {args.train_steps} steps, {data.shape[0]} rows, {time.perf_counter() - t0:.1f} s")
 
 
-def prompts_for(args, rank: int, vocab: int, device) -> torch.Tensor:
-    g = torch.Generator().manual_seed(1234 + rank)
-    return torch.randint(0, vocab, (args.batch, args.prompt_len), generator=g).to(device)
+# ---- the reference arm: the unmodified reference only -----------------------------------------------------------
+
+def import_reference():
+    """``(economize, None)`` from ``baseline/_ref`` (a ``pip --target`` install, a source tree or a site-packages
+    layout), else ``(None, why)``."""
+    ref_dir = os.path.join(HERE, "baseline", "_ref")
+    if not os.path.isdir(ref_dir):
+        return None, f"{ref_dir} does not exist (install the reference there)"
+    roots = [ref_dir, os.path.join(ref_dir, "src")]
+    roots += sorted(glob.glob(os.path.join(ref_dir, "lib", "python*", "site-packages")))
+    roots += sorted(glob.glob(os.path.join(ref_dir, "lib64", "python*", "site-packages")))
+    found = [r for r in roots if os.path.isfile(os.path.join(r, "economize", "__init__.py"))]
+    if not found:
+        return None, f"no economize package under {ref_dir} (looked in {', '.join(roots)})"
+    sys.path.insert(0, found[0])
+    try:
+        import economize
+    except Exception as err:  # the reason goes into the unavailable line
+        return None, f"import economize from {found[0]} failed: {type(err).__name__}: {err}"
+    if not os.path.abspath(economize.__file__).startswith(os.path.abspath(ref_dir)):
+        return None, f"economize resolved to {economize.__file__}, not the copy in {ref_dir}"
+    return economize, None
 
 
-def decode_config(args):
-    import economize_b200 as eco
+class RefArm:
+    """The reference (economize on ``transformers``) behind the recipe's interface."""
 
-    return eco.DecodeConfig(cycle_length=TREE["depth"] + 1, draft_policy="dynamic_tree",
-                            draft_policy_options=dict(TREE), cuda_graphs=not args.no_graphs)
+    def __init__(self, ref, hf, args) -> None:
+        from economize.techniques.eagle3 import Eagle3Config
+
+        self.ref, self.hf, self.args = ref, hf, args
+        self.vocab = hf.config.vocab_size
+        self.model = ref.apply(hf, Eagle3Config(draft_vocab=min(DRAFT_VOCAB, self.vocab), param_dtype="model"))
+        self.tech = self.model.techniques["eagle3"]
+        self.spec_cfg = ref.DecodeConfig(cycle_length=TREE["depth"] + 1, draft_policy="dynamic_tree",
+                                         draft_policy_options=dict(TREE), cuda_graphs=not args.no_graphs)
+        self.plain_cfg = ref.DecodeConfig(cycle_length=1, cuda_graphs=not args.no_graphs)
+
+    def decode(self, prompts, plain: bool):
+        return self.model.decode_batch(list(prompts), self.args.new_tokens,
+                                       decoding=self.plain_cfg if plain else self.spec_cfg)
+
+    def state_shapes(self):
+        return {k: tuple(v.shape) for k, v in self.tech.state_dict().items()}
+
+    def lm_head(self):
+        return self.hf.lm_head.weight
+
+    def state(self):
+        return self.tech.state_dict()
+
+    def load_state(self, state):
+        cur = self.tech.state_dict()
+        self.tech.load_state_dict({k: v.to(cur[k].device, cur[k].dtype) for k, v in state.items()}, strict=True)
+
+    def fit(self, data, steps: int, seed: int):
+        from economize.train import fit
+
+        fit(self.model, data, steps=steps, batch_size=min(4, data.shape[0]), seed=seed, lr=1e-3, warmup_steps=10,
+            log_every=max(1, steps))
+
+
+def run_reference(args, world, rank, log):
+    ref, why = import_reference()
+    if ref is None:
+        return None, why
+    if args.parallel == "tp" and world > 1:
+        return run_reference_tp(ref, args, world, rank, log)
+    import economize.attention
+
+    economize.attention.install()
+    prompts = prompts_for(args, rank, hf_config(args.model).vocab_size)
+    errors = []
+    for attn in ([args.attn] if args.attn else ["economize", "sdpa", "eager"]):
+        hf = build_hf_target(args.model, attn)
+        arm = RefArm(ref, hf, args)
+        try:  # the implementation must serve a tree cycle and a plain step on this box
+            arm.decode(prompts[:, :64], plain=False)
+            arm.decode(prompts[:, :64], plain=True)
+        except Exception as err:
+            errors.append(f"{attn}: {type(err).__name__}: {str(err)[:200]}")
+            log(f"reference attention {attn!r} cannot run: {err}")
+            arm.model.detach()
+            del arm, hf
+            torch.cuda.empty_cache()
+            continue
+        arm.attn = attn
+        break
+    else:
+        return None, "reference decoding failed with every attention implementation: " + " | ".join(errors)
+    train_drafter(arm, args, prompts, _cache_path(args, "reference", rank), log)
+    rows = list(prompts)
+    results = {"cfg": arm.spec_cfg, "attn": arm.attn, "streams": world}
+
+    def step():
+        results["r"] = arm.model.decode_batch(rows, args.new_tokens, decoding=arm.spec_cfg)
+
+    return (arm.model, step, results, prompts), None
+
+
+def run_reference_tp(ref, args, world, rank, log):
+    """The reference's tensor parallelism: ``transformers``' ``tp_plan="auto"`` through
+    ``economize.distributed.tp.load_tensor_parallel`` on a checkpoint of the benchmark weights (written once on the
+    box), with the drafter the 1-GPU reference run trained (or trained here)."""
+    import torch.distributed as dist
+
+    import economize.attention
+    from economize.distributed.tp import load_tensor_parallel
+
+    economize.attention.install()
+    ckpt = os.path.join(CACHE_DIR, f"hf-{args.model}")
+    if rank == 0 and not os.path.isfile(os.path.join(ckpt, "config.json")):
+        hf = build_hf_target(args.model, "sdpa")
+        os.makedirs(CACHE_DIR, exist_ok=True)
+        hf.save_pretrained(ckpt + f".{os.getpid()}")
+        os.replace(ckpt + f".{os.getpid()}", ckpt)
+        del hf
+        torch.cuda.empty_cache()
+    dist.barrier()
+    errors = []
+    for attn in ([args.attn] if args.attn else ["economize", "sdpa"]):
+        try:
+            hf = load_tensor_parallel(ckpt, dtype=torch.bfloat16, attn_implementation=attn)
+            arm = RefArm(ref, hf, args)
+            prompts = prompts_for(args, 0, arm.vocab)
+            arm.decode(prompts[:, :64], plain=False)
+        except Exception as err:
+            errors.append(f"{attn}: {type(err).__name__}: {str(err)[:200]}")
+            continue
+        arm.attn = attn
+        break
+    else:
+        return None, "reference tensor-parallel decoding failed: " + " | ".join(errors)
+    path = _cache_path(args, "reference", 0)
+    if os.path.exists(path):
+        arm.load_state(torch.load(path, map_location="cuda", weights_only=True))
+    else:
+        try:
+            train_drafter(arm, args, prompts, path + f".tp{world}.r{rank}", log)
+        except Exception as err:
+            return None, f"reference drafter training on a tensor-parallel model failed: {err}"
+    rows = list(prompts)
+    results = {"cfg": arm.spec_cfg, "attn": arm.attn, "streams": 1}
+
+    def step():
+        results["r"] = arm.model.decode_batch(rows, args.new_tokens, decoding=arm.spec_cfg)
+
+    return (arm.model, step, results, prompts), None
+
+
+# ---- our arm ------------------------------------------------------------------------------------------------------
+
+class OursArm:
+    def __init__(self, target, args) -> None:
+        import economize_b200 as eco
+        from economize_b200.techniques.eagle3 import Eagle3Config
+
+        self.eco, self.args = eco, args
+        self.target = target
+        self.vocab = target.config.vocab_size
+        self.model = eco.apply(target, Eagle3Config(draft_vocab=min(DRAFT_VOCAB, self.vocab)))
+        self.tech = self.model.techniques["eagle3"]
+        self.spec_cfg = eco.DecodeConfig(cycle_length=TREE["depth"] + 1, draft_policy="dynamic_tree",
+                                         draft_policy_options=dict(TREE), cuda_graphs=not args.no_graphs)
+        self.plain_cfg = eco.DecodeConfig(cycle_length=1, cuda_graphs=not args.no_graphs)
+
+    def decode(self, prompts, plain: bool):
+        return self.model.decode_batch(list(prompts), self.args.new_tokens,
+                                       decoding=self.plain_cfg if plain else self.spec_cfg)
+
+    def state_shapes(self):
+        from economize_b200.techniques.eagle3.formats import to_reference_state
+
+        return {k: tuple(v.shape) for k, v in to_reference_state(self.tech).items()}
+
+    def lm_head(self):
+        return self.target.head_weight
+
+    def state(self):
+        from economize_b200.techniques.eagle3.formats import to_reference_state
+
+        return to_reference_state(self.tech)
+
+    def load_state(self, state):
+        from economize_b200.techniques.eagle3.formats import from_reference_state
+
+        from_reference_state(self.tech, state)
+
+    def fit(self, data, steps: int, seed: int):
+        from economize_b200.train import fit
+
+        fit(self.model, data, steps=steps, batch_size=min(4, data.shape[0]), seed=seed, lr=1e-3, warmup_steps=10,
+            log_every=max(1, steps))
+
+
+def build_target(args):
+    from economize_b200.models.llama import CausalLM
+
+    hf = build_hf_target(args.model)
+    target = CausalLM.from_hf(hf)
+    del hf
+    torch.cuda.empty_cache()
+    return target
+
+
+def run_ours(args, world, rank, log):
+    target = build_target(args)
+    tp = args.parallel == "tp" and world > 1
+    stream = 0 if tp else rank
+    prompts = prompts_for(args, stream, target.config.vocab_size)
+    arm = OursArm(target, args)
+    if tp:
+        import torch.distributed as dist
+
+        from economize_b200.distributed import TPGroup, tensor_parallel
+
+        path = _cache_path(args, "ours", 0)
+        if rank == 0:
+            train_drafter(arm, args, prompts, path, log)
+        dist.barrier()
+        if rank != 0:
+            train_drafter(arm, args, prompts, path, log)  # loads rank 0's weights
+        for tensor in arm.tech.state_dict().values():  # bit-identical drafters: every rank drafts the same tree
+            dist.broadcast(tensor, src=0)
+        tensor_parallel(arm.model, TPGroup(rank, world), fused=not args.nccl_tp)
+    else:
+        train_drafter(arm, args, prompts, _cache_path(args, "ours", stream), log)
+    rows = list(prompts)
+    results = {"cfg": arm.spec_cfg, "streams": 1 if tp else world, "plain_cfg": arm.plain_cfg}
+
+    def step():
+        results["r"] = arm.model.decode_batch(rows, args.new_tokens, decoding=arm.spec_cfg)
+
+    return arm.model, step, results, prompts
 
 
 def acceptance(rows) -> tuple[int, int]:
@@ -304,8 +540,8 @@ def count_launches(step) -> int:
     """Kernels of this package launched by one step (CUPTI trace of an extra, untimed step)."""
     from torch.profiler import ProfilerActivity, profile
 
-    names = ("ecz::", "gemm_swapab", "attn_tc", "attn_merge", "rmsnorm_kernel", "rope_store", "silu_mul",
-             "argmax_kernel", "greedy_accept", "kv_compact", "splitk_reduce")
+    names = ("ecz::", "gemm_", "attn_", "rmsnorm_kernel", "rope_store", "silu_mul", "argmax_kernel",
+             "greedy_accept", "kv_compact", "splitk_reduce", "topk_logp", "tree_", "push_", "reduce_rmsnorm")
     with profile(activities=[ProfilerActivity.CUDA]) as prof:
         step()
         torch.cuda.synchronize()
@@ -316,97 +552,36 @@ def count_launches(step) -> int:
     return count
 
 
-def run_ours(args, world, rank):
-    target = build_target(args)
-    vocab = target.config.vocab_size
-    if args.parallel == "tp" and world > 1:
-        return run_ours_tp(args, world, rank, target)
-    prompts = prompts_for(args, rank, vocab, "cuda")
-    em, _ = build_drafter(target, args, rank, world, prompts)
-    cfg = decode_config(args)
-    rows = list(prompts)
-    results = {"cfg": cfg}
-
-    def step():
-        results["r"] = em.decode_batch(rows, args.new_tokens, decoding=cfg)
-
-    return em, step, results, prompts
-
-
-def run_ours_tp(args, world, rank, target):
-    """One request stream served by all ranks: the target sharded over them, the drafter replicated."""
-    import torch.distributed as dist
-
-    from economize_b200.distributed import TPGroup, tensor_parallel
-
-    prompts = prompts_for(args, 0, target.config.vocab_size, "cuda")  # the same stream on every rank
-    if rank == 0:
-        em, state = build_drafter(target, args, 0, 1, prompts)
-    dist.barrier()
-    if rank != 0:
-        em, state = build_drafter(target, args, 0, 1, prompts)  # loads rank 0's cached weights
-    tech = em.techniques["eagle3"]
-    # bit-identical drafters on every rank (every rank must draft the same tree)
-    for tensor in tech.state_dict().values():
-        dist.broadcast(tensor, src=0)
-    tensor_parallel(em, TPGroup(rank, world), fused=not args.nccl_tp)
-    cfg = decode_config(args)
-    rows = list(prompts)
-    results = {"cfg": cfg}
-
-    def step():
-        results["r"] = em.decode_batch(rows, args.new_tokens, decoding=cfg)
-
-    return em, step, results, prompts
-
-
-def run_reference(args, world, rank):
-    ref = reference_module()
-    if ref is None:
-        return None, "reference not importable from baseline/_ref"
-    if args.parallel == "tp" and world > 1:
-        return None, ("the reference's tensor parallelism loads a checkpoint from disk with transformers' "
-                      "tp_plan='auto'; this benchmark's random-init weights exist only in memory")
-    from economize.techniques.eagle3 import Eagle3Config as RefEagle3Config
-
-    target = build_target(args)
-    vocab = target.config.vocab_size
-    prompts = prompts_for(args, rank, vocab, "cuda")
-    hf = hf_twin(target)
-    _, dstate = build_drafter(target, args, rank, world, prompts, hf=hf)
-    del target, _
-    torch.cuda.empty_cache()
-    model = ref.apply(hf, RefEagle3Config(draft_vocab=min(32000, vocab), param_dtype="model"))
-    tech = model.techniques["eagle3"]
-    current = tech.state_dict()
-    tech.load_state_dict({k: v.to(current[k].device, current[k].dtype) for k, v in dstate.items()}, strict=True)
-    cfg = ref.DecodeConfig(cycle_length=TREE["depth"] + 1, draft_policy="dynamic_tree",
-                           draft_policy_options=dict(TREE), cuda_graphs=not args.no_graphs)
-    rows = list(prompts)
-    results = {"cfg": cfg}
-
-    def step():
-        results["r"] = model.decode_batch(rows, args.new_tokens, decoding=cfg)
-
-    return (model, step, results, prompts), None
-
-
 def main() -> None:
     args = parse()
     sys.path.insert(0, HERE)
     if not torch.cuda.is_available():
-        print(json.dumps({"metric": METRIC, "unavailable": "no CUDA device"}))
+        out = {"metric": METRIC, "unavailable": "no CUDA device"}
+        if args.impl == "reference":
+            out["impl"] = "reference"
+        print(json.dumps(out))
         return
-    world, rank, local = setup_dist(args)
+    world, rank, local = setup_dist()
+
+    def log(msg: str) -> None:
+        print(f"[bench r{rank}] {msg}", file=sys.stderr, flush=True)
+
+    tp = args.parallel == "tp" and world > 1
     if args.impl == "reference":
-        built, why = run_reference(args, world, rank)
-        if built is None:
+        built, why = run_reference(args, world, rank, log)
+        ok = reduce_sum(0.0 if built is None else 1.0, world)
+        if ok < world:  # every rank takes the same collective steps: all stop when one cannot run
             if rank == 0:
-                print(json.dumps({"impl": "reference", "unavailable": why}))
+                print(json.dumps({"impl": "reference", "unavailable": why or "another rank could not build the "
+                                  "reference"}))
+            if world > 1:
+                import torch.distributed as dist
+
+                dist.destroy_process_group()
             return
         model, step, results, prompts = built
     else:
-        model, step, results, prompts = run_ours(args, world, rank)
+        model, step, results, prompts = run_ours(args, world, rank, log)
 
     for _ in range(args.warmup):
         step()
@@ -424,11 +599,12 @@ def main() -> None:
         barrier(world)
     ms = start.elapsed_time(end) / args.steps
     ms_max = reduce_max(ms, world)
-    streams = 1 if (args.parallel == "tp" and world > 1) else world
+    streams = results["streams"]
     new_tokens = args.batch * args.new_tokens * streams
     value = new_tokens / (ms_max / 1e3)
     accepted, cycles = acceptance(results["r"])
-    tau_local = 1.0 + accepted / cycles if cycles else None
+    tau_local = 1.0 + accepted / cycles if cycles else 0.0
+    spec_tokens = [r.tokens.cpu() for r in results["r"]]
 
     # ---- end to end through the public API: pinned host prompts in, host tokens out ----
     host_prompts = [p.cpu().pin_memory() for p in prompts]
@@ -446,31 +622,33 @@ def main() -> None:
     torch.cuda.synchronize()
     e2e_ms = reduce_max((time.perf_counter() - t0) * 1e3 / e2e_steps, world)
     launches = None
+    equal_plain = None
     if args.impl == "ours":
         try:
             launches = count_launches(step) * args.steps
         except Exception:
             launches = None
-    tau = None
-    if tau_local is not None:
-        tau = reduce_sum(tau_local, world) / world
+        # lossless check: the speculative tokens equal plain greedy decoding through the same engine
+        plain = model.decode_batch(list(prompts), args.new_tokens, decoding=results["plain_cfg"])
+        equal_plain = all(torch.equal(a, b.tokens.cpu()) for a, b in zip(spec_tokens, plain))
+    tau = reduce_sum(tau_local, world) / world
     if rank == 0:
+        parallelism = (f"tp{world}" + ("-nccl" if args.nccl_tp and args.impl == "ours" else
+                                       "-fused" if args.impl == "ours" else "-hf-auto")) if tp else f"dp{world}"
         line = {
             "metric": METRIC, "value": round(value, 2), "unit": "tok/s", "n_gpus": world, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": round(ms_max, 3), "higher_is_better": True,
-            "scaling": "strong" if (args.parallel == "tp" and world > 1) else "weak",
+            "scaling": "strong" if tp else "weak",
             "vs_baseline": (value / BASELINE_TOKS) if BASELINE_TOKS else None, "dtype": "bf16",
             "data": "synthetic (uniform-random prompts, random-init weights)",
-            "mean_accepted_len": round(tau, 4) if tau is not None else None,
+            "mean_accepted_len": round(tau, 4),
             "config": {"model": "Llama-3.1-8B arch" if args.model == "llama31_8b" else "tiny",
-                       "drafter": "EAGLE-3 (draft vocab 32000), dynamic tree depth 6 topk 10 nodes 60; trained "
-                                  f"{args.train_steps} steps in {args.train_rounds} rounds on the greedy and "
-                                  "speculative trajectories of both implementations on the benchmark prompts (same "
-                                  "weights in both arms)",
+                       "drafter": f"EAGLE-3 (draft vocab {DRAFT_VOCAB}), dynamic tree depth 6 topk 10 nodes 60; "
+                                  f"trained {args.train_steps} steps in {args.train_rounds} rounds by the arm's own "
+                                  "train.fit on its own greedy and speculative trajectories of the benchmark prompts "
+                                  "(same initialisation and recipe in both arms)",
                        "global_batch": args.batch * streams, "seq_len": args.prompt_len,
-                       "new_tokens": args.new_tokens,
-                       "parallelism": (f"tp{world}" + ("-nccl" if args.nccl_tp else "-fused"))
-                       if (args.parallel == "tp" and world > 1) else f"dp{world}",
+                       "new_tokens": args.new_tokens, "parallelism": parallelism,
                        "train_steps": args.train_steps, "cuda_graphs": not args.no_graphs,
                        "l2": "weights (16 GB) exceed L2; no flush"},
             "clocks": clocks.summary(),
@@ -479,16 +657,19 @@ def main() -> None:
                     "d2h_bytes_per_step": sum(t.numel() * t.element_size() for t in toks) * streams},
             "gpu_launches": launches,
         }
+        if equal_plain is not None:
+            line["tokens_equal_plain_greedy"] = equal_plain
         if args.impl == "reference":
             line["impl"] = "reference"
-        print(json.dumps(line))
+            line["config"]["attn_implementation"] = results.get("attn")
+        print(json.dumps(line), flush=True)
     # release the captured graphs (they may hold NCCL calls) and the NVLink buffers before the group goes away
     engine_model = getattr(model, "model", None)
     if hasattr(model, "refresh"):
         model.refresh()
-    tp = getattr(engine_model, "tp", None)
-    if tp is not None and getattr(tp, "comm", None) is not None:
-        tp.comm.close()
+    tpg = getattr(engine_model, "tp", None)
+    if tpg is not None and getattr(tpg, "comm", None) is not None:
+        tpg.comm.close()
     results.clear()
     del step, model
     import gc
