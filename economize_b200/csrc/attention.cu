@@ -731,12 +731,8 @@ int launch_attention(const void* q, const CUtensorMap* tm_k, const CUtensorMap* 
   if (mask != nullptr && T > 64) return -1;
   const bool fp8 = k_scale != nullptr;
   if (fp8 && v_scale == nullptr) return -1;
-  static bool configured = false;
-  if (!configured) {
-    cudaFuncSetAttribute(attn_tc_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmem);
-    cudaFuncSetAttribute(attn_tc_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmem);
-    configured = true;
-  }
+  set_max_smem(attn_tc_kernel<false>, kSmem);
+  set_max_smem(attn_tc_kernel<true>, kSmem);
   const int ctas = B * Hkv * plan.m_tiles;
   float* ws_o = plan.splits > 1 ? ws : nullptr;
   float* ws_ml = plan.splits > 1 ? ws + static_cast<size_t>(ctas) * plan.splits * kRows * kDim : nullptr;
@@ -758,11 +754,7 @@ int launch_attention_scores(const void* q, const CUtensorMap* tm_k, const float*
                             const int* kv_len, const int* n_new, const int64_t* mask, int B, int T, int H, int Hkv,
                             int D, int S, float scale, int q_offset, unsigned* status, cudaStream_t stream) {
   if (D != kDim || H % Hkv != 0 || (mask != nullptr && T > 64)) return -1;
-  static bool configured = false;
-  if (!configured) {
-    cudaFuncSetAttribute(attn_scores_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kScoreSmem);
-    configured = true;
-  }
+  set_max_smem(attn_scores_kernel, kScoreSmem);
   const int G = H / Hkv;
   const int m_tiles = (T * G + kRows - 1) / kRows;
   dim3 grid(B * Hkv * m_tiles, (S + kKeys - 1) / kKeys);

@@ -12,6 +12,10 @@
 #include <cuda_runtime.h>
 #include <stdint.h>
 
+#include <mutex>
+#include <set>
+#include <utility>
+
 namespace ecz {
 
 using bf16 = __nv_bfloat16;
@@ -69,16 +73,17 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
 }
 
 // Wait until the phase of parity `parity` of `bar` completed. Returns false (and sets `code` in *status) when the
-// wait exceeds kWaitLimitNs or when *abort became non-zero (another role of the CTA gave up already).
+// wait exceeds `limit_ns` (kWaitLimitNs by default) or when *abort became non-zero (another role of the CTA gave up
+// already).
 __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, unsigned* status, unsigned code,
-                                          volatile int* abort) {
+                                          volatile int* abort, unsigned long long limit_ns = kWaitLimitNs) {
   if (mbar_try_wait(bar, parity)) return true;
   const unsigned long long start = global_timer_ns();
   for (uint32_t i = 1;; ++i) {
     if (mbar_try_wait(bar, parity)) return true;
     if ((i & 63u) == 0u) {
       if (abort != nullptr && *abort) return false;
-      if (global_timer_ns() - start > kWaitLimitNs) {
+      if (global_timer_ns() - start > limit_ns) {
         if (status != nullptr) atomicOr(status, code);
         if (abort != nullptr) *abort = 1;
         return false;
@@ -223,6 +228,27 @@ __device__ __forceinline__ void pdl_trigger() { asm volatile("griddepcontrol.lau
 __device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
 
 bool pdl_enabled();
+
+// Raise a kernel's dynamic shared-memory limit on the CURRENT device. The attribute belongs to the (kernel, device)
+// pair, so a process that launches on several GPUs must set it on each; this records which pairs are done (under a
+// lock, so host threads may launch concurrently) and sets each one once.
+inline cudaError_t set_max_smem(const void* kernel, int bytes) {
+  static std::mutex mu;
+  static std::set<std::pair<const void*, int>> done;
+  int device = 0;
+  cudaError_t err = cudaGetDevice(&device);
+  if (err != cudaSuccess) return err;
+  std::lock_guard<std::mutex> lock(mu);
+  if (done.count({kernel, device}) != 0) return cudaSuccess;
+  err = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
+  if (err == cudaSuccess) done.insert({kernel, device});
+  return err;
+}
+
+template <typename... KArgs>
+inline cudaError_t set_max_smem(void (*kernel)(KArgs...), int bytes) {
+  return set_max_smem(reinterpret_cast<const void*>(kernel), bytes);
+}
 
 template <typename... KArgs, typename... Args>
 inline cudaError_t launch_pdl(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t stream,

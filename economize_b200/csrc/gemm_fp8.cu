@@ -237,11 +237,7 @@ template <int BN>
 int run_fp8(const CUtensorMap& tm_w, const CUtensorMap& tm_x, const CUtensorMap& tm_sx, const float* sw, void* y,
             float* ws, int M, int N, int K, int splits, unsigned* status, cudaStream_t stream) {
   using Cfg = Fp8Cfg<BN>;
-  static bool configured = false;
-  if (!configured) {
-    cudaFuncSetAttribute(gemm_fp8_kernel<BN>, cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg::kSmem);
-    configured = true;
-  }
+  set_max_smem(gemm_fp8_kernel<BN>, Cfg::kSmem);
   const int total_kb = K / kBK;
   const int kbps = (total_kb + splits - 1) / splits;
   splits = (total_kb + kbps - 1) / kbps;

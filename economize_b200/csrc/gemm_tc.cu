@@ -275,14 +275,8 @@ int run_gemm(const CUtensorMap& tm_w, const CUtensorMap& tm_x, void* y, float* w
              int K, int splits, unsigned* status, cudaStream_t stream, const PeerOut& peer, int flags = 0) {
   constexpr int kOcc2 = split_occupancy<BN>();
   const bool occ2 = (flags & 1) != 0 && kOcc2 == 2;
-  static bool configured = false;
-  if (!configured) {
-    cudaFuncSetAttribute(gemm_swapab_kernel<BN, 1>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                         GemmCfg<BN, 1>::kSmem);
-    cudaFuncSetAttribute(gemm_swapab_kernel<BN, kOcc2>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                         GemmCfg<BN, kOcc2>::kSmem);
-    configured = true;
-  }
+  set_max_smem(gemm_swapab_kernel<BN, 1>, GemmCfg<BN, 1>::kSmem);
+  set_max_smem(gemm_swapab_kernel<BN, kOcc2>, GemmCfg<BN, kOcc2>::kSmem);
   const int total_kb = (K + kBK - 1) / kBK;
   const int kbps = (total_kb + splits - 1) / splits;
   splits = (total_kb + kbps - 1) / kbps;  // no empty split
@@ -469,11 +463,7 @@ template <int BN>
 int run_gemm_cluster(const CUtensorMap& tm_w, const CUtensorMap& tm_x, void* y, int M, int N, int K, int splits,
                      unsigned* status, cudaStream_t stream, const PeerOut& peer) {
   using Cfg = GemmCfg<BN, split_occupancy<BN>()>;
-  static bool configured = false;
-  if (!configured) {
-    cudaFuncSetAttribute(gemm_cluster_kernel<BN>, cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg::kSmem);
-    configured = true;
-  }
+  set_max_smem(gemm_cluster_kernel<BN>, Cfg::kSmem);
   const int total_kb = (K + kBK - 1) / kBK;
   const int kbps = (total_kb + splits - 1) / splits;
   splits = (total_kb + kbps - 1) / kbps;
@@ -722,11 +712,7 @@ template <int BN>
 int run_gemm_persistent(const CUtensorMap& tm_w, const CUtensorMap& tm_x, void* y, float* ws, int* counters, int M,
                         int N, int K, int ctas, unsigned* status, cudaStream_t stream) {
   using Cfg = GemmCfg<BN>;
-  static bool configured = false;
-  if (!configured) {
-    cudaFuncSetAttribute(gemm_persistent_kernel<BN>, cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg::kSmem);
-    configured = true;
-  }
+  set_max_smem(gemm_persistent_kernel<BN>, Cfg::kSmem);
   launch_pdl(gemm_persistent_kernel<BN>, dim3(ctas), dim3(192), Cfg::kSmem, stream, tm_w, tm_x,
              static_cast<bf16*>(y), ws, counters, M, N, K, status);
   return 0;
@@ -767,11 +753,14 @@ int gemm_cluster_splits(int M, int N, int K, int num_sms) {
 template <int BN>
 int cluster_capacity_bn(int splits) {
   using Cfg = GemmCfg<BN, split_occupancy<BN>()>;
-  static int cache[9] = {0};
+  static std::mutex mu;
+  static int cache[64][9] = {};  // per device (the occupancy query reads the device's own attributes)
   if (splits < 1 || splits > 8) return 0;
-  if (cache[splits] == 0) {
-    cudaFuncSetAttribute(gemm_cluster_kernel<BN>, cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg::kSmem);
-    cudaFuncSetAttribute(gemm_cluster_kernel<BN>, cudaFuncAttributeNonPortableClusterSizeAllowed, 0);
+  int device = 0;
+  if (cudaGetDevice(&device) != cudaSuccess || device < 0 || device >= 64) return 1;
+  std::lock_guard<std::mutex> lock(mu);
+  if (cache[device][splits] == 0) {
+    set_max_smem(gemm_cluster_kernel<BN>, Cfg::kSmem);
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(splits, 1, splits);
     cfg.blockDim = dim3(128);
@@ -788,9 +777,9 @@ int cluster_capacity_bn(int splits) {
       cudaGetLastError();
       n = 1;
     }
-    cache[splits] = std::max(1, n);
+    cache[device][splits] = std::max(1, n);
   }
-  return cache[splits];
+  return cache[device][splits];
 }
 
 int gemm_cluster_capacity(int M, int splits) {
@@ -914,7 +903,11 @@ extern "C" __attribute__((visibility("default"))) int ecz_linear_bf16_noalloc(co
   if (scratch == nullptr) return -4;
   unsigned* status = reinterpret_cast<unsigned*>(scratch + ECZ_NOALLOC_SCRATCH_FLOATS);
   cudaStream_t s = static_cast<cudaStream_t>(stream);
-  cudaMemsetAsync(status, 0, sizeof(unsigned), s);  // the status word starts every call cleared
+  const cudaError_t clear = cudaMemsetAsync(status, 0, sizeof(unsigned), s);  // every call starts with a clear word
+  if (clear != cudaSuccess) {
+    std::fprintf(stderr, "ecz_linear_bf16_noalloc: clearing the status word failed: %s\n", cudaGetErrorString(clear));
+    return -6;
+  }
   CUtensorMap tm_w, tm_x;
   if (ecz::make_tmap_2d_bf16(&tm_w, w, N, K, K, 128) != 0 ||
       ecz::make_tmap_2d_bf16(&tm_x, x, M, K, K, ecz::gemm_block_n(M)) != 0) {
@@ -930,4 +923,50 @@ extern "C" __attribute__((visibility("default"))) int ecz_linear_bf16_noalloc(co
     return -6;
   }
   return 0;
+}
+
+extern "C" __attribute__((visibility("default"))) int ecz_linear_bf16_noalloc_status(unsigned* status_out) {
+  int device = -1;
+  if (status_out == nullptr) return -1;
+  if (cudaGetDevice(&device) != cudaSuccess) return -5;
+  float* scratch = noalloc_scratch_for_current_device(device);
+  if (scratch == nullptr) return -4;
+  // a synchronous 4-byte copy into the caller's host memory (pageable: no allocation on either side)
+  const cudaError_t err = cudaMemcpy(status_out, scratch + ECZ_NOALLOC_SCRATCH_FLOATS, sizeof(unsigned),
+                                     cudaMemcpyDeviceToHost);
+  if (err != cudaSuccess) {
+    std::fprintf(stderr, "ecz_linear_bf16_noalloc_status: reading the status word failed: %s\n",
+                 cudaGetErrorString(err));
+    return -6;
+  }
+  return 0;
+}
+
+namespace {
+
+// One thread waits on an mbarrier that nothing completes, bounded by `limit_ns`: the wait runs out, records
+// kStatusWaitFull in the status word and the kernel returns. No copy or MMA is in flight when it gives up.
+__global__ void noalloc_wait_selftest_kernel(unsigned* status, unsigned long long limit_ns) {
+  __shared__ uint64_t bar;
+  if (threadIdx.x == 0) {
+    ecz::mbar_init(&bar, 1);
+    ecz::fence_mbar_init();
+    ecz::mbar_wait(&bar, 0, status, ecz::kStatusWaitFull, nullptr, limit_ns);
+  }
+}
+
+}  // namespace
+
+extern "C" __attribute__((visibility("default"))) int ecz_noalloc_wait_selftest(unsigned long long limit_ns,
+                                                                                 void* stream) {
+  int device = -1;
+  if (cudaGetDevice(&device) != cudaSuccess) return -5;
+  if (limit_ns == 0 || limit_ns > 1000000000ull) return -1;
+  float* scratch = noalloc_scratch_for_current_device(device);
+  if (scratch == nullptr) return -4;
+  unsigned* status = reinterpret_cast<unsigned*>(scratch + ECZ_NOALLOC_SCRATCH_FLOATS);
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  if (cudaMemsetAsync(status, 0, sizeof(unsigned), s) != cudaSuccess) return -6;
+  noalloc_wait_selftest_kernel<<<1, 32, 0, s>>>(status, limit_ns);
+  return cudaGetLastError() == cudaSuccess ? 0 : -6;
 }

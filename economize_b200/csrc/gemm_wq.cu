@@ -396,11 +396,7 @@ template <int FMT, int BN>
 int run_wq(const WqMaps& maps, void* y, int M, int N, int K, int group, int splits, unsigned* status,
            cudaStream_t stream) {
   using Cfg = WqCfg<FMT, BN>;
-  static bool configured = false;
-  if (!configured) {
-    cudaFuncSetAttribute(gemm_wq_kernel<FMT, BN>, cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg::kSmem);
-    configured = true;
-  }
+  set_max_smem(gemm_wq_kernel<FMT, BN>, Cfg::kSmem);
   const int total_kb = K / kBK;
   const int kbps = (total_kb + splits - 1) / splits;
   splits = (total_kb + kbps - 1) / kbps;

@@ -230,11 +230,7 @@ template <int BN>
 int run_grouped(const CUtensorMap& tm_w, const CUtensorMap& tm_x, void* y, const int* seg_start, const int* seg_end,
                 const int* seg_expert, int G, int max_rows, int N, int K, unsigned* status, cudaStream_t stream) {
   using Cfg = GroupedCfg<BN>;
-  static bool configured = false;
-  if (!configured) {
-    cudaFuncSetAttribute(gemm_grouped_kernel<BN>, cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg::kSmem);
-    configured = true;
-  }
+  set_max_smem(gemm_grouped_kernel<BN>, Cfg::kSmem);
   dim3 grid((N + kBM - 1) / kBM, (max_rows + BN - 1) / BN, G);
   launch_pdl(gemm_grouped_kernel<BN>, grid, dim3(128), Cfg::kSmem, stream, tm_w, tm_x, static_cast<bf16*>(y),
              seg_start, seg_end, seg_expert, N, K, status);

@@ -67,3 +67,67 @@ def test_noalloc_rejects_oversized(noalloc, cuda):
     bad = torch.zeros(5, 12, device=cuda, dtype=torch.bfloat16)  # K not a multiple of 8
     assert _call(noalloc, bad, torch.zeros(8, 12, device=cuda, dtype=torch.bfloat16),
                  torch.empty(5, 8, device=cuda, dtype=torch.bfloat16)) == -1
+
+
+@pytest.fixture(scope="module")
+def noalloc_status(cuda):
+    import economize_b200._C as ext
+
+    lib = ctypes.CDLL(ext.__file__)
+    status = lib.ecz_linear_bf16_noalloc_status
+    status.restype = ctypes.c_int
+    status.argtypes = [ctypes.POINTER(ctypes.c_uint)]
+    selftest = lib.ecz_noalloc_wait_selftest
+    selftest.restype = ctypes.c_int
+    selftest.argtypes = [ctypes.c_ulonglong, ctypes.c_void_p]
+    return status, selftest
+
+
+def _status(status_fn) -> int:
+    word = ctypes.c_uint(12345)
+    assert status_fn(ctypes.byref(word)) == 0
+    return word.value
+
+
+def test_noalloc_status_word(noalloc, noalloc_status, cuda):
+    """The status word a bounded wait writes reaches the caller: a clean call reads 0, a wait that runs out (the
+    self-test waits 1 ms on a barrier nothing completes) reads its code, and the next call clears it again."""
+    from economize_b200 import ops
+
+    status_fn, selftest = noalloc_status
+    g = torch.Generator(device=cuda).manual_seed(3)
+    x = torch.randn(61, 4096, device=cuda, generator=g).bfloat16()
+    w = (torch.randn(4096, 4096, device=cuda, generator=g) * 0.02).bfloat16()
+    y = torch.empty(61, 4096, device=cuda, dtype=torch.bfloat16)
+    assert _call(noalloc, x, w, y) == 0
+    torch.cuda.synchronize()
+    assert _status(status_fn) == 0
+    assert selftest(1_000_000, torch.cuda.current_stream().cuda_stream) == 0
+    torch.cuda.synchronize()
+    assert _status(status_fn) == 1
+    assert _call(noalloc, x, w, y) == 0
+    torch.cuda.synchronize()
+    assert _status(status_fn) == 0
+    expect = ops.linear(x, w)
+    torch.testing.assert_close(y.float(), expect.float(), atol=2e-2 * expect.abs().max().item() / 4 + 1e-3,
+                               rtol=2e-2)
+    assert selftest(0, None) == -1  # the limit must be positive
+
+
+@pytest.mark.skipif(not torch.cuda.is_available() or torch.cuda.device_count() < 2, reason="needs two GPUs")
+def test_noalloc_second_device(noalloc, cuda):
+    """Each device gets its own scratch address and kernel attributes: the entry point on cuda:1 after cuda:0."""
+    from economize_b200 import ops
+
+    for dev in (0, 1):
+        d = torch.device("cuda", dev)
+        with torch.cuda.device(d):
+            g = torch.Generator(device=d).manual_seed(5)
+            x = torch.randn(61, 4096, device=d, generator=g).bfloat16()
+            w = (torch.randn(6144, 4096, device=d, generator=g) * 0.02).bfloat16()
+            y = torch.empty(61, 6144, device=d, dtype=torch.bfloat16)
+            assert _call(noalloc, x, w, y) == 0
+            torch.cuda.synchronize(d)
+            expect = ops.linear(x, w)
+            torch.testing.assert_close(y.float(), expect.float(),
+                                       atol=2e-2 * expect.abs().max().item() / 4 + 1e-3, rtol=2e-2)
