@@ -16,6 +16,15 @@
 // and (bit j of mask[b, t], or j <= q_offset + t without a mask). The key range may be split over `splits` CTAs,
 // whose (O, max, sum) partials a merge kernel combines in log-sum-exp form (the split-K merge of the reference).
 //
+// Exact-tail mode (tail_w > 0, decode and verification passes): a query at position p takes the keys at positions
+// below p - tail_w from the tensor-core walk above, by absolute slot (they are committed keys at slot = position in
+// every pass), and the keys at positions [p - tail_w, p] in the merge kernel, one at a time in position order on the
+// CUDA cores: committed slots first, then the query's own new keys (its ancestors and itself) in depth order. How a
+// key enters the sum then depends only on the query's and the key's positions, never on where a draft tree put the
+// key or how many queries share the pass, so a verification pass computes every accepted token's attention bit for
+// bit as a one-token pass at the same position does (greedy speculative decoding reproduces plain decoding exactly)
+// as long as the tree is at most tail_w deep.
+//
 // fp8 caches (e4m3 codes with one static scale per KV head, K = s_k * K8, V = s_v * V8): TMA brings the raw
 // [128 keys, 128 B] code tiles into a double-buffered staging ring, all threads convert them to bf16 (exact: every
 // e4m3 value is a bf16 value) in the swizzled layout the UMMAs read, and the scales are applied outside the tensor
@@ -207,7 +216,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                    int chunks_per_split, int m_tiles, unsigned* status, unsigned long long* trace,
                    const float* __restrict__ k_scale, const float* __restrict__ v_scale,
                    const uint32_t* __restrict__ keep, float* __restrict__ lse_out,
-                   const uint8_t* __restrict__ kivi, const int* __restrict__ kivi_chunks, int kivi_bits) {
+                   const uint8_t* __restrict__ kivi, const int* __restrict__ kivi_chunks, int kivi_bits, int tail_w) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* q_tile = smem;
@@ -249,7 +258,14 @@ __global__ void __launch_bounds__(kThreads, 1)
   const int causal_lim = q_offset + t + 1;
 
   const int t_last = min(T - 1, ((m_tile + 1) * kRows - 1) / G);
-  int visible_end = use_mask ? base + nn : base + min(nn, q_offset + t_last + 1);
+  const bool tail = tail_w > 0;
+  // exact-tail mode: this row's tensor-core keys are the committed slots below its position minus tail_w
+  int tc_lim = 0;
+  if (tail && row_valid) {
+    const int depth = use_mask ? (__popcll(bits) - 1) : (q_offset + t);
+    tc_lim = max(0, min(base, base + depth - tail_w));
+  }
+  int visible_end = tail ? base : use_mask ? base + nn : base + min(nn, q_offset + t_last + 1);
   visible_end = min(visible_end, S);
   const int n_chunks = (visible_end + kKeys - 1) / kKeys;
   const int c0 = split * chunks_per_split;
@@ -381,7 +397,8 @@ __global__ void __launch_bounds__(kThreads, 1)
     float sc[32];
     tmem_ld16(tmem_s + lane_off, sc);
     tmem_ld16(tmem_s + lane_off + 16, sc + 16);
-    uint32_t vis = visible32(c * kKeys + col0, base, nn, use_mask, bits, causal_lim, row_valid);
+    uint32_t vis = tail ? visible32(c * kKeys + col0, tc_lim, 0, false, 0ull, 0, row_valid)
+                        : visible32(c * kKeys + col0, base, nn, use_mask, bits, causal_lim, row_valid);
     if (keep != nullptr) {  // evicted committed slots are invisible (new slots are never evicted)
       const int s0 = c * kKeys + col0;
       const uint32_t kw = keep[(static_cast<size_t>(b) * Hkv + kvh) * (S / 32) + s0 / 32];
@@ -466,7 +483,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   }
 
   if (!failed && row_valid) {
-    if (splits == 1) {
+    if (splits == 1 && !tail) {
       if (lse_out != nullptr && quarter == 0)  // log2-domain log-sum-exp of the row's scaled scores
         lse_out[(static_cast<size_t>(b) * T + t) * H + head] = l_tot > 0.f ? m_run + __log2f(l_tot) : -INFINITY;
       const float inv = l_tot > 0.f ? 1.f / l_tot : 0.f;
@@ -506,6 +523,110 @@ __global__ void __launch_bounds__(128) attn_merge_kernel(const float* __restrict
   pdl_wait();
   merge_row(ws_o, ws_ml, out, blockIdx.x, blockIdx.y * 4 + (threadIdx.x >> 5), threadIdx.x & 31, T, H, Hkv, m_tiles,
             splits, lse_out);
+}
+
+// Exact-tail merge: one warp per packed row combines the tensor-core partials of every split with the row's tail
+// keys (positions [p - tail_w, p]), which it attends itself in position order. Lane l owns dimensions 4l .. 4l + 3;
+// a score is the lane products summed in a fixed order and then over the warp by a butterfly, so every lane holds
+// the same value, and it is computed the same way in both passes over the tail (max, then weights).
+__device__ __forceinline__ float4 load_kv4(const uint8_t* base, size_t row, int lane, bool fp8) {
+  if (fp8) {
+    const uint32_t w = *reinterpret_cast<const uint32_t*>(base + row * kDim + lane * 4);
+    float4 v;
+    const __half2 lo = __half2(__nv_cvt_fp8x2_to_halfraw2(static_cast<__nv_fp8x2_storage_t>(w & 0xFFFFu), __NV_E4M3));
+    const __half2 hi = __half2(__nv_cvt_fp8x2_to_halfraw2(static_cast<__nv_fp8x2_storage_t>(w >> 16), __NV_E4M3));
+    const float2 a = __half22float2(lo), b = __half22float2(hi);
+    v.x = a.x; v.y = a.y; v.z = b.x; v.w = b.y;
+    return v;
+  }
+  const uint2 w = *reinterpret_cast<const uint2*>(base + (row * kDim + lane * 4) * 2);
+  const float2 a = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&w.x));
+  const float2 b = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&w.y));
+  return make_float4(a.x, a.y, b.x, b.y);
+}
+
+__device__ __forceinline__ float tail_score(const float4& qv, const float4& kv, float scale_log2) {
+  float d = qv.x * kv.x;
+  d = fmaf(qv.y, kv.y, d);
+  d = fmaf(qv.z, kv.z, d);
+  d = fmaf(qv.w, kv.w, d);
+  return warp_sum(d) * scale_log2;
+}
+
+__global__ void __launch_bounds__(128) attn_merge_tail_kernel(
+    const float* __restrict__ ws_o, const float* __restrict__ ws_ml, bf16* __restrict__ out, int T, int H, int Hkv,
+    int m_tiles, int splits, float* __restrict__ lse_out, const bf16* __restrict__ q,
+    const uint8_t* __restrict__ k_cache, const uint8_t* __restrict__ v_cache, const int* __restrict__ kv_len,
+    const int* __restrict__ n_new, const int64_t* __restrict__ mask, int S, float scale_log2, int q_offset,
+    int tail_w, const float* __restrict__ k_scale, const float* __restrict__ v_scale,
+    const uint32_t* __restrict__ keep) {
+  pdl_trigger();
+  pdl_wait();
+  const int tile = blockIdx.x, r = blockIdx.y * 4 + (threadIdx.x >> 5), lane = threadIdx.x & 31;
+  const int m_tile = tile % m_tiles, bh = tile / m_tiles;
+  const int b = bh / Hkv, kvh = bh % Hkv;
+  const int G = H / Hkv;
+  const int p = m_tile * kRows + r;
+  const int t = p / G;
+  if (t >= T) return;
+  const int head = kvh * G + p % G;
+  const bool fp8 = k_scale != nullptr;
+  const float sl = fp8 ? scale_log2 * k_scale[kvh] : scale_log2;
+  const float sv = fp8 ? v_scale[kvh] : 1.f;
+  const int base = kv_len[b], nn = n_new[b];
+  const bool use_mask = mask != nullptr;
+  const uint64_t bits = use_mask ? static_cast<uint64_t>(mask[static_cast<size_t>(b) * T + t]) : 0ull;
+  const int depth = use_mask ? (__popcll(bits) - 1) : (q_offset + t);
+  const int lo = max(0, base + depth - tail_w);
+  const size_t row0 = (static_cast<size_t>(b) * Hkv + kvh) * S;
+  const float4 qv = load_kv4(reinterpret_cast<const uint8_t*>(q),
+                             (static_cast<size_t>(b) * T + t) * H + head, lane, false);
+  auto committed_visible = [&](int s) -> bool {
+    return keep == nullptr || ((keep[(static_cast<size_t>(b) * Hkv + kvh) * (S / 32) + s / 32] >> (s & 31)) & 1u);
+  };
+  auto new_visible = [&](int j) -> bool { return use_mask ? ((bits >> j) & 1ull) != 0ull : j <= q_offset + t; };
+  const int n_end = min(nn, use_mask ? 64 : q_offset + t + 1);
+
+  // the maximum over the splits' partials and the tail's scores
+  float mx = -INFINITY;
+  for (int sp = 0; sp < splits; ++sp) {
+    const size_t slot = (static_cast<size_t>(tile) * splits + sp) * kRows + r;
+    if (ws_ml[slot * 2 + 1] > 0.f) mx = fmaxf(mx, ws_ml[slot * 2]);
+  }
+  for (int s = lo; s < base; ++s)
+    if (committed_visible(s)) mx = fmaxf(mx, tail_score(qv, load_kv4(k_cache, row0 + s, lane, fp8), sl));
+  for (int j = 0; j < n_end; ++j)
+    if (new_visible(j)) mx = fmaxf(mx, tail_score(qv, load_kv4(k_cache, row0 + base + j, lane, fp8), sl));
+
+  float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+  float denom = 0.f;
+  for (int sp = 0; sp < splits; ++sp) {
+    const size_t slot = (static_cast<size_t>(tile) * splits + sp) * kRows + r;
+    const float l = ws_ml[slot * 2 + 1];
+    if (!(l > 0.f)) continue;
+    const float w = exp2f(ws_ml[slot * 2] - mx);
+    const float4 v = reinterpret_cast<const float4*>(ws_o + slot * kDim)[lane];
+    acc.x += v.x * w; acc.y += v.y * w; acc.z += v.z * w; acc.w += v.w * w;
+    denom += l * w;
+  }
+  auto add_key = [&](size_t row) {
+    const float w = exp2f(tail_score(qv, load_kv4(k_cache, row, lane, fp8), sl) - mx);
+    float4 v = load_kv4(v_cache, row, lane, fp8);
+    v.x *= sv; v.y *= sv; v.z *= sv; v.w *= sv;
+    acc.x += v.x * w; acc.y += v.y * w; acc.z += v.z * w; acc.w += v.w * w;
+    denom += w;
+  };
+  for (int s = lo; s < base; ++s)
+    if (committed_visible(s)) add_key(row0 + s);
+  for (int j = 0; j < n_end; ++j)
+    if (new_visible(j)) add_key(row0 + base + j);
+
+  const float inv = denom > 0.f ? 1.f / denom : 0.f;
+  if (lse_out != nullptr && lane == 0)
+    lse_out[(static_cast<size_t>(b) * T + t) * H + head] = denom > 0.f ? mx + __log2f(denom) : -INFINITY;
+  bf16* dst = out + ((static_cast<size_t>(b) * T + t) * H + head) * kDim + lane * 4;
+  *reinterpret_cast<__nv_bfloat162*>(dst) = __floats2bfloat162_rn(acc.x * inv, acc.y * inv);
+  *reinterpret_cast<__nv_bfloat162*>(dst + 2) = __floats2bfloat162_rn(acc.z * inv, acc.w * inv);
 }
 
 // ---- attention scores for KV eviction (H2O / SnapKV / PyramidKV) -------------------------------------------------
@@ -706,7 +827,7 @@ __global__ void kivi_advance_kernel(const int* __restrict__ kv_len, int* __restr
 
 // The split over keys depends on the batch, the KV heads and the cache size only (not on the number of query
 // tokens), so a one-token pass and a verification pass reduce a row's keys in the same order.
-AttnPlan attention_plan(int B, int T, int H, int Hkv, int S, int num_sms) {
+AttnPlan attention_plan(int B, int T, int H, int Hkv, int S, int num_sms, bool tail) {
   AttnPlan plan;
   const int G = H / Hkv;
   plan.m_tiles = (T * G + kRows - 1) / kRows;
@@ -717,7 +838,8 @@ AttnPlan attention_plan(int B, int T, int H, int Hkv, int S, int num_sms) {
   plan.chunks_per_split = (total_chunks + splits - 1) / splits;
   plan.splits = (total_chunks + plan.chunks_per_split - 1) / plan.chunks_per_split;
   const long ctas = static_cast<long>(heads) * plan.m_tiles;
-  plan.ws_floats = plan.splits > 1 ? ctas * plan.splits * kRows * (kDim + 2) : 0;
+  plan.ws_floats = (plan.splits > 1 || tail) ? ctas * plan.splits * kRows * (kDim + 2) : 0;
+  plan.tail = tail;
   return plan;
 }
 
@@ -725,8 +847,11 @@ int launch_attention(const void* q, const CUtensorMap* tm_k, const CUtensorMap* 
                      const int* kv_len, const int* n_new, const int64_t* mask, int B, int T, int H, int Hkv, int D,
                      int S, float scale, int q_offset, const AttnPlan& plan, unsigned* status, cudaStream_t stream,
                      unsigned long long* trace, const float* k_scale, const float* v_scale, const uint32_t* keep,
-                     float* lse_out, const uint8_t* kivi, const int* kivi_chunks, int kivi_bits) {
+                     float* lse_out, const uint8_t* kivi, const int* kivi_chunks, int kivi_bits, int tail_w,
+                     const void* k_cache, const void* v_cache) {
   if (kivi != nullptr && (k_scale != nullptr || (kivi_bits != 2 && kivi_bits != 4))) return -1;
+  if (tail_w < 0 || tail_w > 64 || (tail_w > 0 && (!plan.tail || k_cache == nullptr || v_cache == nullptr)))
+    return -1;
   if (D != kDim || H % Hkv != 0) return -1;
   if (mask != nullptr && T > 64) return -1;
   const bool fp8 = k_scale != nullptr;
@@ -734,14 +859,22 @@ int launch_attention(const void* q, const CUtensorMap* tm_k, const CUtensorMap* 
   set_max_smem(attn_tc_kernel<false>, kSmem);
   set_max_smem(attn_tc_kernel<true>, kSmem);
   const int ctas = B * Hkv * plan.m_tiles;
-  float* ws_o = plan.splits > 1 ? ws : nullptr;
-  float* ws_ml = plan.splits > 1 ? ws + static_cast<size_t>(ctas) * plan.splits * kRows * kDim : nullptr;
+  const bool staged = plan.splits > 1 || tail_w > 0;  // partials go through the workspace and a merge
+  float* ws_o = staged ? ws : nullptr;
+  float* ws_ml = staged ? ws + static_cast<size_t>(ctas) * plan.splits * kRows * kDim : nullptr;
   dim3 grid(ctas, plan.splits);
   launch_pdl(fp8 ? attn_tc_kernel<true> : attn_tc_kernel<false>, grid, dim3(kThreads), kSmem, stream,
              static_cast<const bf16*>(q), *tm_k, *tm_v, static_cast<bf16*>(out), ws_o, ws_ml, kv_len, n_new, mask, T,
              H, Hkv, S, scale * 1.4426950408889634f, q_offset, plan.chunks_per_split, plan.m_tiles, status, trace,
-             k_scale, v_scale, keep, lse_out, kivi, kivi_chunks, kivi_bits);
-  if (plan.splits > 1) {
+             k_scale, v_scale, keep, lse_out, kivi, kivi_chunks, kivi_bits, tail_w);
+  if (tail_w > 0) {
+    dim3 mgrid(ctas, kRows / 4);
+    launch_pdl(attn_merge_tail_kernel, mgrid, dim3(128), 0, stream, static_cast<const float*>(ws_o),
+               static_cast<const float*>(ws_ml), static_cast<bf16*>(out), T, H, Hkv, plan.m_tiles, plan.splits,
+               lse_out, static_cast<const bf16*>(q), static_cast<const uint8_t*>(k_cache),
+               static_cast<const uint8_t*>(v_cache), kv_len, n_new, mask, S, scale * 1.4426950408889634f, q_offset,
+               tail_w, k_scale, v_scale, keep);
+  } else if (plan.splits > 1) {
     dim3 mgrid(ctas, kRows / 4);
     launch_pdl(attn_merge_kernel, mgrid, dim3(128), 0, stream, static_cast<const float*>(ws_o),
                static_cast<const float*>(ws_ml), static_cast<bf16*>(out), T, H, Hkv, plan.m_tiles, plan.splits,

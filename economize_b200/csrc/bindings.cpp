@@ -224,10 +224,11 @@ Tensor rope_store(Tensor qkv, Tensor positions, Tensor cos, Tensor sin, int64_t 
 Tensor attention(Tensor q, Tensor k_cache, Tensor v_cache, Tensor kv_len, Tensor n_new, c10::optional<Tensor> mask,
                  double scale, int64_t q_offset, c10::optional<Tensor> trace, c10::optional<Tensor> k_scale,
                  c10::optional<Tensor> v_scale, c10::optional<Tensor> keep, c10::optional<Tensor> lse_out,
-                 c10::optional<Tensor> kivi, c10::optional<Tensor> kivi_chunks, int64_t kivi_bits) {
+                 c10::optional<Tensor> kivi, c10::optional<Tensor> kivi_chunks, int64_t kivi_bits, int64_t tail) {
   CHECK_CUDA(q);
   CHECK_BF16(q);
   TORCH_CHECK(q.dim() == 4 && q.size(3) == 128 && k_cache.dim() == 4, "attention: head_dim must be 128");
+  TORCH_CHECK(tail >= 0 && tail <= 64, "attention: the exact tail covers 0 .. 64 positions");
   const bool fp8 = fp8_cache(k_cache, k_scale, v_scale, k_cache.size(1));
   TORCH_CHECK(v_cache.scalar_type() == k_cache.scalar_type(), "K and V caches must share a dtype");
   CHECK_I32(kv_len);
@@ -274,7 +275,8 @@ Tensor attention(Tensor q, Tensor k_cache, Tensor v_cache, Tensor kv_len, Tensor
                 "lse_out must be fp32 [B, T, H]");
   }
   auto out = at::empty_like(q);
-  const ecz::AttnPlan plan = ecz::attention_plan(B, T, H, Hkv, S, num_sms(q.get_device()));
+  if (tail > 0) TORCH_CHECK(T <= 64, "attention: the exact tail serves passes of at most 64 query tokens");
+  const ecz::AttnPlan plan = ecz::attention_plan(B, T, H, Hkv, S, num_sms(q.get_device()), tail > 0);
   Tensor ws;
   if (plan.ws_floats > 0) ws = at::empty({plan.ws_floats}, q.options().dtype(at::kFloat));
   const uint64_t rows = static_cast<uint64_t>(B) * Hkv * S;
@@ -298,7 +300,8 @@ Tensor attention(Tensor q, Tensor k_cache, Tensor v_cache, Tensor kv_len, Tensor
                                        lse_out.has_value() ? lse_out->data_ptr<float>() : nullptr,
                                        kivi.has_value() ? kivi->data_ptr<uint8_t>() : nullptr,
                                        kivi.has_value() ? kivi_chunks->data_ptr<int>() : nullptr,
-                                       static_cast<int>(kivi_bits));
+                                       static_cast<int>(kivi_bits), static_cast<int>(tail), k_cache.data_ptr(),
+                                       v_cache.data_ptr());
   TORCH_CHECK(rc == 0, "attention: unsupported shape (head_dim must be 128, H divisible by H_kv)");
   return out;
 }
@@ -1204,7 +1207,8 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
         py::arg("q"), py::arg("k_cache"), py::arg("v_cache"), py::arg("kv_len"), py::arg("n_new"), py::arg("mask"),
         py::arg("scale"), py::arg("q_offset"), py::arg("trace") = py::none(), py::arg("k_scale") = py::none(),
         py::arg("v_scale") = py::none(), py::arg("keep") = py::none(), py::arg("lse_out") = py::none(),
-        py::arg("kivi") = py::none(), py::arg("kivi_chunks") = py::none(), py::arg("kivi_bits") = 0);
+        py::arg("kivi") = py::none(), py::arg("kivi_chunks") = py::none(), py::arg("kivi_bits") = 0,
+        py::arg("tail") = 0);
   m.def("kivi_chunk_size", &ecz::kivi_chunk_size, "bytes of one KIVI-coded 128-key chunk");
   m.def("kivi_quantize", &kivi_quantize, "quantise committed cache chunks to KIVI codes and advance the counts");
   m.def("attention_scores", &attention_scores, "accumulate KV-eviction attention scores (tcgen05)");

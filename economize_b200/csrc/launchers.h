@@ -27,6 +27,7 @@ struct AttnPlan {
   int splits = 1;
   int chunks_per_split = 1;
   long ws_floats = 0;
+  bool tail = false;  // exact-tail mode: partials always staged in the workspace
 };
 
 // elementwise.cu
@@ -73,13 +74,14 @@ int launch_gemm_persistent(const CUtensorMap* tm_w, const CUtensorMap* tm_x, voi
                            int N, int K, int num_sms, unsigned* status, cudaStream_t stream);
 
 // attention.cu
-AttnPlan attention_plan(int B, int T, int H, int Hkv, int S, int num_sms);
+AttnPlan attention_plan(int B, int T, int H, int Hkv, int S, int num_sms, bool tail = false);
 int launch_attention(const void* q, const CUtensorMap* tm_k, const CUtensorMap* tm_v, void* out, float* ws,
                      const int* kv_len, const int* n_new, const int64_t* mask, int B, int T, int H, int Hkv, int D,
                      int S, float scale, int q_offset, const AttnPlan& plan, unsigned* status, cudaStream_t stream,
                      unsigned long long* trace = nullptr, const float* k_scale = nullptr,
                      const float* v_scale = nullptr, const uint32_t* keep = nullptr, float* lse_out = nullptr,
-                     const uint8_t* kivi = nullptr, const int* kivi_chunks = nullptr, int kivi_bits = 0);
+                     const uint8_t* kivi = nullptr, const int* kivi_chunks = nullptr, int kivi_bits = 0,
+                     int tail_w = 0, const void* k_cache = nullptr, const void* v_cache = nullptr);
 // KIVI: bytes of one quantized 128-key chunk; quantise committed chunks of a bf16 cache [L, 2, B, Hkv, S, D] into
 // kivi [L, B, Hkv, S / 128, chunk bytes] and advance chunks [B] (at most max_new chunks per row and call)
 int kivi_chunk_size(int bits);

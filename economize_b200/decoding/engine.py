@@ -291,7 +291,7 @@ class SpecEngine:
             n = (lengths - start).clamp(0, end - start).to(torch.int32)
             kv = torch.clamp(lengths, max=start).to(torch.int32)
             pos = (start + torch.arange(end - start, device=prompts.device, dtype=torch.int32)).expand(batch, -1)
-            h, a = self.model.forward_step(part, StepBatch(kv, n, pos.contiguous()), st.cache, capture)
+            h, a = self.model.forward_step(part, StepBatch(kv, n, pos.contiguous(), prompt=True), st.cache, capture)
             hs.append(h)
             auxes.append(a)
         hidden = torch.cat(hs, 1)

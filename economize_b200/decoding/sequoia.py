@@ -9,14 +9,18 @@ have children. The exact pass verifies it as any draft tree, so decoding stays l
 
 ``acceptance[r]`` is the probability that the exact model's token after an accepted node is the drafter's ``r``-th
 most likely token (or one such vector per depth of the parent node, the root's first and the last reused below).
-The events are disjoint across siblings, so a tree's expected tokens per cycle is the sum over its nodes of the
-product of the rates along the node's rank path, plus one for the root. :func:`sequoia_tree` maximizes this over
-trees of at most ``total_tokens`` nodes and depth at most ``depth`` by dynamic programming: ``G[l][n]`` is the best
-value of a subtree of at most ``n`` nodes whose root has depth ``l``, and the root's children are placed rank by
-rank as a knapsack over the remaining ``n - 1`` nodes (a rank may also be left out, so measured rates that are not
-decreasing are used as they are). With measured latencies (``verify_latency[i]``: one exact pass over ``i + 1``
-tokens; ``draft_latency``: one draft step) the size and depth are those of the most tokens per second, which is
-Sequoia's hardware-aware choice.
+Siblings are disjoint events, so a node contributes its *reach* (the product of the rates along its rank path) to
+the expected tokens per cycle, and a tree's value is one (the root) plus the reaches of its nodes.
+
+Shape search. A node's reach never exceeds its parent's (every factor is at most one), so among all sets of ``n``
+rank paths of depth at most ``D`` that are closed under taking parents, the ``n`` paths of largest reach are one
+(ties go to the shallower path, which keeps every parent ahead of its children) and no other set has a larger sum.
+:func:`sequoia_tree` therefore grows the tree best-first from a heap of candidate children: it takes the candidate of
+largest reach and offers that node's children, until ``total_tokens`` nodes are placed or no candidate reaches
+anything. Ranks that a measured profile makes worth less than a higher rank are simply placed later (siblings need
+not be consecutive ranks). With measured latencies (``verify_latency[i]``: one exact pass over ``i + 1`` tokens;
+``draft_latency``: one draft step) every prefix of the best-first order, for every depth limit, is a candidate, and
+the one of most tokens per second wins (Sequoia's hardware-aware choice).
 
 :func:`measure_acceptance` estimates the rates by decoding prompts with a probe tree and counting which rank the
 exact token had at every accepted node; an explicit tree can be given as rank ``paths`` instead (the format of
@@ -25,6 +29,7 @@ Medusa's tree choices).
 
 from __future__ import annotations
 
+import heapq
 from collections.abc import Mapping, Sequence
 from dataclasses import dataclass, field
 
@@ -43,7 +48,8 @@ MAX_FORWARDED = 64  # ancestor bits of the drafter's tree steps are one 64-bit w
 
 @dataclass(frozen=True)
 class StaticTree:
-    """A draft tree as rank paths, sorted by depth then rank (so every parent precedes its children).
+    """A draft tree as rank paths in breadth-first order (by depth, then lexicographically), so that every node
+    comes after its parent.
 
     Attributes:
         paths: ``paths[i]`` is the rank path of node ``i`` (``(0, 2)``: the 3rd best token after the best first
@@ -56,16 +62,24 @@ class StaticTree:
 
     @classmethod
     def from_paths(cls, paths: Sequence[Sequence[int]], expected: float | None = None) -> StaticTree:
-        clean = sorted({tuple(int(r) for r in p) for p in paths}, key=lambda q: (len(q), q))
-        if not clean:
-            raise ConfigError("a static draft tree needs at least one path")
-        have = set(clean)
-        for p in clean:
-            if not p or any(r < 0 for r in p):
-                raise ConfigError(f"tree path {p} must be a non-empty sequence of ranks >= 0")
-            if len(p) > 1 and p[:-1] not in have:
-                raise ConfigError(f"tree path {p} has no parent path {p[:-1]}")
-        return cls(tuple(clean), expected)
+        unique: set[Path] = set()
+        for raw in paths:
+            path = tuple(int(r) for r in raw)
+            if len(path) == 0:
+                raise ConfigError("an empty rank path names the root, which every tree has implicitly; list only "
+                                  "draft nodes")
+            bad = [r for r in path if r < 0]
+            if bad:
+                raise ConfigError(f"ranks are 0-based positions in the drafter's ranking; {path} holds {bad[0]}")
+            unique.add(path)
+        if not unique:
+            raise ConfigError("the draft tree has no nodes")
+        orphans = [p for p in unique if len(p) > 1 and p[:-1] not in unique]
+        if orphans:
+            p = min(orphans, key=lambda q: (len(q), q))
+            raise ConfigError(f"node {p} hangs below {p[:-1]}, which is not in the tree")
+        ordered = sorted(unique, key=lambda q: (len(q), q))
+        return cls(tuple(ordered), expected)
 
     @property
     def size(self) -> int:
@@ -73,95 +87,83 @@ class StaticTree:
 
     @property
     def depth(self) -> int:
-        return max(len(p) for p in self.paths)
+        return max(map(len, self.paths))
 
     @property
     def parents(self) -> tuple[int, ...]:
         """Parent node of every node (``-1``: a child of the root)."""
-        index = {p: i for i, p in enumerate(self.paths)}
-        return tuple(index[p[:-1]] if len(p) > 1 else -1 for p in self.paths)
+        where = {path: i for i, path in enumerate(self.paths)}
+        return tuple(-1 if len(path) == 1 else where[path[:-1]] for path in self.paths)
 
     @property
     def ranks(self) -> tuple[int, ...]:
-        return tuple(p[-1] for p in self.paths)
+        return tuple(path[-1] for path in self.paths)
 
     @property
     def forwarded(self) -> int:
         """Nodes that run through the drafter (those with children)."""
-        return len({p[:-1] for p in self.paths if len(p) > 1})
+        return len({path[:-1] for path in self.paths} - {()})
 
 
-def _rates(acceptance: Sequence[float] | Sequence[Sequence[float]], depth: int) -> np.ndarray:
-    """The rates as a matrix ``[depth, R]``: row ``l`` holds the rates after a node of depth ``l`` (root: 0)."""
-    rows = acceptance if len(acceptance) and isinstance(acceptance[0], (Sequence, np.ndarray)) else [acceptance]
-    rows = [[float(v) for v in row] for row in rows]
-    width = max((len(r) for r in rows), default=0)
+def rate_table(acceptance: Sequence[float] | Sequence[Sequence[float]], depth: int) -> np.ndarray:
+    """``acceptance`` as a ``[depth, width]`` table: row ``l`` holds the rates after a node of depth ``l`` (the root
+    is depth 0); a single vector serves every depth, and per-depth vectors repeat their last one downwards."""
+    nested = len(acceptance) > 0 and isinstance(acceptance[0], (Sequence, np.ndarray))
+    vectors = [list(map(float, v)) for v in (acceptance if nested else [acceptance])]
+    width = max(map(len, vectors), default=0)
     if width == 0:
-        raise ConfigError("the acceptance vector is empty")
-    for row in rows:
-        if any(not 0.0 <= v <= 1.0 for v in row) or sum(row) > 1.0 + 1e-6:
-            raise ConfigError(f"acceptance rates {row} must lie in [0, 1] and sum to at most 1 (they are "
-                              "probabilities of disjoint events)")
-    out = np.zeros((depth, width))
+        raise ConfigError("sequoia needs at least one acceptance rate")
+    for v in vectors:
+        low, total = min(v, default=0.0), sum(v)
+        if low < 0.0 or max(v, default=0.0) > 1.0:
+            raise ConfigError(f"acceptance rates are probabilities; {v} has an entry outside [0, 1]")
+        if total > 1.0 + 1e-6:
+            raise ConfigError(f"the exact token can match at most one rank, so the rates of one depth sum to at "
+                              f"most 1; {v} sums to {total:.4f}")
+    table = np.zeros((depth, width))
     for level in range(depth):
-        row = rows[min(level, len(rows) - 1)]
-        out[level, :len(row)] = row
-    return out
+        v = vectors[level] if level < len(vectors) else vectors[-1]
+        table[level, :len(v)] = v
+    return table
+
+
+def _reach_of(path: Path, table: np.ndarray) -> float:
+    reach = 1.0
+    for level, rank in enumerate(path):
+        reach *= table[level, rank] if rank < table.shape[1] else 0.0
+    return reach
 
 
 def expected_tokens(tree: StaticTree | Sequence[Sequence[int]],
                     acceptance: Sequence[float] | Sequence[Sequence[float]]) -> float:
     """Expected tokens per cycle of ``tree`` (the root's token included) under the rates ``acceptance``."""
-    if not isinstance(tree, StaticTree):
-        tree = StaticTree.from_paths(tree)
-    p = _rates(acceptance, tree.depth)
-    reach: dict[Path, float] = {(): 1.0}
-    for path in tree.paths:
-        level, rank = len(path) - 1, path[-1]
-        reach[path] = reach[path[:-1]] * (p[level, rank] if rank < p.shape[1] else 0.0)
-    return float(sum(reach.values()))
+    tree = tree if isinstance(tree, StaticTree) else StaticTree.from_paths(tree)
+    table = rate_table(acceptance, tree.depth)
+    return 1.0 + float(sum(_reach_of(path, table) for path in tree.paths))
 
 
-def _solve(p: np.ndarray, nodes: int) -> tuple[np.ndarray, list[list[np.ndarray]]]:
-    """Dynamic program over the rate matrix ``p [D, R]``: ``G [D + 1, nodes + 1]`` and, for every level and rank,
-    the subtree size given to that rank's child for every remaining budget (0: the rank is left out)."""
-    depth, ranks = p.shape
-    g = np.zeros((depth + 1, nodes + 1))
-    g[depth, 1:] = 1.0  # a node at the largest depth has no children
-    m = np.arange(nodes + 1)[:, None]
-    t = np.arange(nodes + 1)[None, :]
-    fits = (t >= 1) & (t <= m)
-    rest = np.clip(m - t, 0, nodes)
-    sizes: list[list[np.ndarray]] = [[] for _ in range(depth)]
-    for level in range(depth - 1, -1, -1):
-        h = np.zeros(nodes + 1)  # best use of a budget by the ranks after the current one
-        per_rank: list[np.ndarray] = []
-        for rank in range(ranks - 1, -1, -1):
-            gain = np.where(fits, p[level, rank] * g[level + 1][t] + h[rest], -np.inf)
-            best_t = gain.argmax(1)
-            best = gain[np.arange(nodes + 1), best_t]
-            take = best > h + 1e-15
-            per_rank.append(np.where(take, best_t, 0))
-            h = np.where(take, best, h)
-        sizes[level] = per_rank[::-1]
-        g[level, 1:] = 1.0 + h[:-1]
-    return g, sizes
+def best_first(table: np.ndarray, limit: int, depth: int) -> list[tuple[Path, float]]:
+    """Up to ``limit`` rank paths of depth at most ``depth`` in decreasing reach (ties: shallower, then smaller
+    ranks first), each with its reach; paths of zero reach are never taken. Every prefix of the result is a tree."""
+    width = table.shape[1]
+    heap: list[tuple[float, int, Path]] = []
 
+    def offer(parent: Path, reach: float) -> None:
+        level = len(parent)
+        if level >= depth:
+            return
+        for rank in range(width):
+            r = reach * table[level, rank]
+            if r > 0.0:
+                heapq.heappush(heap, (-r, level + 1, parent + (rank,)))
 
-def _paths(sizes: list[list[np.ndarray]], level: int, nodes: int, prefix: Path, out: list[Path]) -> None:
-    """Append the rank paths of the best subtree of ``nodes`` nodes rooted at ``prefix`` (of depth ``level``)."""
-    budget = nodes - 1
-    if level >= len(sizes):
-        return
-    for rank, table in enumerate(sizes[level]):
-        if budget <= 0:
-            break
-        take = int(table[budget])
-        if take:
-            child = prefix + (rank,)
-            out.append(child)
-            _paths(sizes, level + 1, take, child, out)
-            budget -= take
+    offer((), 1.0)
+    order: list[tuple[Path, float]] = []
+    while heap and len(order) < limit:
+        neg, _, path = heapq.heappop(heap)
+        order.append((path, -neg))
+        offer(path, -neg)
+    return order
 
 
 def sequoia_tree(acceptance: Sequence[float] | Sequence[Sequence[float]], total_tokens: int, depth: int, *,
@@ -169,43 +171,49 @@ def sequoia_tree(acceptance: Sequence[float] | Sequence[Sequence[float]], total_
     """The Sequoia tree for ``acceptance`` with at most ``total_tokens`` nodes and depth at most ``depth``.
 
     Without ``verify_latency`` the tree maximizes expected tokens per cycle; with it (one entry per exact pass of
-    ``1 .. total_tokens + 1`` tokens) it maximizes expected tokens per second over every size and depth, a cycle of
-    depth ``d`` costing ``verify_latency[n] + d * draft_latency``.
+    ``1 .. total_tokens + 1`` tokens) it maximizes expected tokens per second over every size and depth limit, a
+    cycle whose tree is ``d`` deep costing ``verify_latency[n] + d * draft_latency``.
     """
-    if not (is_positive_int(total_tokens) and is_positive_int(depth)):
-        raise ConfigError(f"a sequoia tree needs total_tokens >= 1 and depth >= 1, got {total_tokens} and {depth}")
+    if not is_positive_int(total_tokens):
+        raise ConfigError(f"total_tokens counts draft nodes and must be a positive integer, got {total_tokens!r}")
+    if not is_positive_int(depth):
+        raise ConfigError(f"depth must be a positive integer, got {depth!r}")
     if draft_latency < 0:
-        raise ConfigError(f"draft_latency must be >= 0, got {draft_latency}")
-    p = _rates(acceptance, depth)
+        raise ConfigError(f"draft_latency is a time and cannot be negative, got {draft_latency}")
+    table = rate_table(acceptance, depth)
     if verify_latency is None:
-        g, sizes = _solve(p, total_tokens + 1)
-        paths: list[Path] = []
-        _paths(sizes, 0, total_tokens + 1, (), paths)
-        if not paths:
-            raise ConfigError("every acceptance rate is 0: no tree adds an expected token")
-        return StaticTree.from_paths(paths, float(g[0, total_tokens + 1]))
-    if len(verify_latency) < total_tokens + 1 or any(float(v) <= 0 for v in verify_latency):
-        raise ConfigError(f"verify_latency needs a positive entry for every pass of 1..{total_tokens + 1} tokens")
-    best: tuple[float, int, int, list] | None = None
-    for d in range(1, depth + 1):
-        g, sizes = _solve(p[:d], total_tokens + 1)
-        for n in range(1, total_tokens + 1):
-            rate = g[0, n + 1] / (float(verify_latency[n]) + d * draft_latency)
-            if best is None or rate > best[0] * (1 + 1e-12):
-                best = (rate, d, n, sizes)
-    _, d, n, sizes = best
-    paths = []
-    _paths(sizes, 0, n + 1, (), paths)
-    if not paths:
-        raise ConfigError("every acceptance rate is 0: no tree adds an expected token")
-    tree = StaticTree.from_paths(paths)
-    return StaticTree(tree.paths, expected_tokens(tree, p[:d].tolist()))
+        order = best_first(table, total_tokens, depth)
+        if not order:
+            raise ConfigError("no draft node can be accepted under these rates (all of them are 0)")
+        return StaticTree.from_paths([p for p, _ in order], 1.0 + sum(r for _, r in order))
+    times = [float(v) for v in verify_latency]
+    if len(times) <= total_tokens or min(times[:total_tokens + 1]) <= 0:
+        raise ConfigError(f"verify_latency must give a positive time for every exact pass of 1 to "
+                          f"{total_tokens + 1} tokens ({total_tokens + 1} entries)")
+    choice: tuple[float, list[Path], float] | None = None
+    for limit in range(1, depth + 1):
+        order = best_first(table[:limit], total_tokens, limit)
+        value, deepest = 1.0, 0
+        for n, (path, reach) in enumerate(order, start=1):
+            value += reach
+            deepest = max(deepest, len(path))
+            speed = value / (times[n] + deepest * draft_latency)
+            if choice is None or speed > choice[0] * (1.0 + 1e-12):
+                choice = (speed, [p for p, _ in order[:n]], value)
+    if choice is None:
+        raise ConfigError("no draft node can be accepted under these rates (all of them are 0)")
+    return StaticTree.from_paths(choice[1], choice[2])
 
 
 def probe_paths(depth: int, width: int) -> tuple[Path, ...]:
-    """A probe tree: a spine of rank-0 nodes ``depth`` deep; the root and every spine node but the last have the
-    children of ranks ``0 .. width - 1``."""
-    return tuple((0,) * level + (rank,) for level in range(depth) for rank in range(width))
+    """The probe tree of :func:`measure_acceptance`: below the root and below each of the first ``depth - 1`` nodes
+    of the all-best spine ``(0,), (0, 0), ...``, the children of ranks ``0 .. width - 1``."""
+    spine: Path = ()
+    out: list[Path] = []
+    for _ in range(depth):
+        out.extend(spine + (rank,) for rank in range(width))
+        spine = spine + (0,)
+    return tuple(out)
 
 
 @dataclass
@@ -254,35 +262,36 @@ _OPTIONS = ("acceptance", "paths", "total_tokens", "depth", "verify_latency", "d
 
 def tree_from_options(options: Mapping[str, object], cycle_length: int) -> tuple[StaticTree, bool]:
     """The tree of the ``sequoia`` policy's options and whether acceptance is recorded."""
-    unknown = sorted(set(options) - set(_OPTIONS))
-    if unknown:
-        raise ConfigError(f"draft_policy 'sequoia' has no options {unknown}; it takes {', '.join(_OPTIONS)}")
+    stray = [name for name in options if name not in _OPTIONS]
+    if stray:
+        raise ConfigError(f"unknown sequoia option(s) {sorted(stray)} (known: {', '.join(_OPTIONS)})")
     record = options.get("record_acceptance", False)
-    if not isinstance(record, bool):
-        raise ConfigError(f"record_acceptance must be a bool, got {record!r}")
-    if ("paths" in options) == ("acceptance" in options):
-        raise ConfigError("draft_policy 'sequoia' needs exactly one of 'acceptance' and 'paths'")
-    if "paths" in options:
-        extra = sorted(set(options) & {"total_tokens", "depth", "verify_latency", "draft_latency"})
-        if extra:
-            raise ConfigError(f"options {extra} shape a tree from 'acceptance'; an explicit 'paths' tree takes none")
+    if record not in (True, False) or not isinstance(record, bool):
+        raise ConfigError(f"record_acceptance is a flag (True or False), not {record!r}")
+    explicit, rated = "paths" in options, "acceptance" in options
+    if explicit and rated:
+        raise ConfigError("give sequoia either an explicit tree ('paths') or the rates to shape one ('acceptance'), "
+                          "not both")
+    if not (explicit or rated):
+        raise ConfigError("sequoia needs a tree: pass 'paths' (rank paths) or 'acceptance' (rates to shape one)")
+    if explicit:
+        shaping = [name for name in ("total_tokens", "depth", "verify_latency", "draft_latency") if name in options]
+        if shaping:
+            raise ConfigError(f"{shaping} only shape a tree from 'acceptance'; with explicit 'paths' drop them")
         tree = StaticTree.from_paths(options["paths"])
     else:
         depth = options.get("depth", max(cycle_length - 1, 1))
         total = options.get("total_tokens", 32)
-        for name, value in (("depth", depth), ("total_tokens", total)):
-            if not is_positive_int(value):
-                raise ConfigError(f"draft_policy 'sequoia' needs a positive integer {name}, got {value!r}")
         draft = options.get("draft_latency", 0.0)
         if isinstance(draft, bool) or not isinstance(draft, (int, float)) or draft < 0:
-            raise ConfigError(f"draft_latency must be a number >= 0, got {draft!r}")
+            raise ConfigError(f"draft_latency is a non-negative time, got {draft!r}")
         latency = options.get("verify_latency")
-        if "draft_latency" in options and latency is None:
-            raise ConfigError("draft_latency needs verify_latency")
-        tree = sequoia_tree(options["acceptance"], int(total), int(depth), verify_latency=latency,
-                            draft_latency=float(draft))
-    if tree.size + 1 > MAX_FORWARDED or tree.forwarded > MAX_FORWARDED:
-        raise ConfigError(f"a verified tree holds at most {MAX_FORWARDED - 1} draft nodes, got {tree.size}")
+        if latency is None and "draft_latency" in options:
+            raise ConfigError("draft_latency only matters next to verify_latency; give both or neither")
+        tree = sequoia_tree(options["acceptance"], total, depth, verify_latency=latency, draft_latency=float(draft))
+    if tree.size >= MAX_FORWARDED or tree.forwarded > MAX_FORWARDED:
+        raise ConfigError(f"the tree has {tree.size} draft nodes; one verified pass holds at most "
+                          f"{MAX_FORWARDED - 1}")
     return tree, record
 
 

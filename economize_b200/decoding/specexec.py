@@ -59,28 +59,34 @@ class SearchOptions:
 
     @classmethod
     def from_options(cls, options: Mapping[str, object], cycle_length: int) -> SearchOptions:
-        names = ("depth", "width", "topk", "total_tokens", "decay")
-        unknown = sorted(set(options) - set(names))
-        if unknown:
-            raise ConfigError(f"draft_policy 'specexec' has no options {unknown}; it takes {', '.join(names)}")
-        values = {"depth": max(cycle_length - 1, 1), "width": 8, "topk": 8, "total_tokens": 60, **options}
-        decay = values.pop("decay", 0.95)
-        if isinstance(decay, bool) or not isinstance(decay, (int, float)) or not 0.0 < decay <= 1.0:
-            raise ConfigError(f"draft_policy 'specexec' needs a decay in (0, 1], got {decay!r}")
-        for name, value in values.items():
-            if not is_positive_int(value):
-                raise ConfigError(f"draft_policy 'specexec' needs a positive integer {name}, got {value!r}")
-        search = cls(int(values["depth"]), int(values["width"]), int(values["topk"]), int(values["total_tokens"]),
-                     float(decay))
-        if search.width > search.topk:
-            raise ConfigError(f"width={search.width} exceeds topk={search.topk}: the first step expands children "
-                              "of the root, of which there are topk")
+        """Parse ``draft_policy_options`` of the ``specexec`` policy (``depth`` defaults to ``cycle_length - 1``),
+        refusing shapes the fixed-size search buffers cannot hold."""
+        known = {"depth": max(cycle_length - 1, 1), "width": 8, "topk": 8, "total_tokens": 60, "decay": 0.95}
+        stray = [name for name in options if name not in known]
+        if stray:
+            raise ConfigError(f"unknown specexec option(s) {sorted(stray)} (known: {', '.join(known)})")
+        merged = dict(known)
+        merged.update(options)
+        sizes = {}
+        for name in ("depth", "width", "topk", "total_tokens"):
+            if not is_positive_int(merged[name]):
+                raise ConfigError(f"specexec's {name} is a count and must be a positive integer, not {merged[name]!r}")
+            sizes[name] = int(merged[name])
+        decay = merged["decay"]
+        if isinstance(decay, bool) or not isinstance(decay, (int, float)) or decay <= 0.0 or decay > 1.0:
+            raise ConfigError(f"specexec's decay scales each deeper level's probability: it lies in (0, 1], "
+                              f"not {decay!r}")
+        search = cls(sizes["depth"], sizes["width"], sizes["topk"], sizes["total_tokens"], float(decay))
         if search.topk > 16:
-            raise ConfigError(f"topk={search.topk}: the fused top-k ranks at most 16 children per node")
+            raise ConfigError(f"topk={search.topk}, but the fused top-k kernel ranks at most 16 children per node")
+        if search.width > search.topk:
+            raise ConfigError(f"width={search.width} exceeds topk={search.topk}: the first search step can only "
+                              "expand the root's topk children")
         if search.total_tokens > search.candidates:
-            raise ConfigError(f"total_tokens={search.total_tokens} exceeds the {search.candidates} candidates of a "
-                              f"search of depth {search.depth}, width {search.width} and topk {search.topk}")
-        if search.total_tokens + 1 > MAX_TREE_NODES or search.forwarded > MAX_TREE_NODES:
-            raise ConfigError(f"a search forwards (depth - 1) * width = {search.forwarded} nodes and drafts "
-                              f"{search.total_tokens}; both must fit {MAX_TREE_NODES}-bit ancestor words")
+            raise ConfigError(f"total_tokens={search.total_tokens} exceeds the {search.candidates} candidates a "
+                              f"search of depth {search.depth}, width {search.width} and topk {search.topk} "
+                              "produces")
+        if max(search.total_tokens + 1, search.forwarded) > MAX_TREE_NODES:
+            raise ConfigError(f"the search forwards {search.forwarded} nodes and verifies {search.total_tokens} + 1; "
+                              f"both must fit the {MAX_TREE_NODES}-bit ancestor words")
         return search

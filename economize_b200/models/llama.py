@@ -86,6 +86,10 @@ class CausalLM(nn.Module):
         self.depth_policy = None  # dynamic depth (per-token layer skipping / early exit) of the exact passes
         self.prefill_sparsity = None  # sparse prefill attention (MInference), run as a chunked prefill
         self.kv_scales: tuple[torch.Tensor, torch.Tensor] | None = None
+        #: decode and verification passes (at most 64 queries) attend the keys of the last ``exact_tail`` positions
+        #: before each query in position order (ops.attention's exact tail), so greedy speculative decoding with
+        #: trees up to this deep reproduces plain greedy decoding bit for bit; 0 turns it off
+        self.exact_tail = 16
         #: tensor-parallel group (set by economize_b200.parallel.tp.shard_model) and this rank's shard sizes
         self.tp = None
         self.local = dict(num_heads=config.num_heads, num_kv_heads=config.num_kv_heads,
@@ -232,8 +236,10 @@ class CausalLM(nn.Module):
             if pattern is not None:
                 keep = pattern if keep is None else keep & pattern
         kivi = self.kv_quantizer.layer_args(index, cache) if self.kv_quantizer is not None else {}
+        sparse_pass = sparse is not None and sparse.active
+        tail = self.exact_tail if (not batch.prompt and q.shape[1] <= 64 and not sparse_pass) else 0
         o = ops.attention(q, k_cache, v_cache, batch.kv_len, batch.n_new, batch.mask, q_offset=batch.q_offset,
-                          k_scale=k_scale, v_scale=v_scale, keep=keep, **kivi)
+                          k_scale=k_scale, v_scale=v_scale, keep=keep, tail=tail, **kivi)
         if self.kv_evictor is not None and batch.is_prefill:
             self.kv_evictor.observe_prefill(index, q, k_cache, v_cache, batch)
         o = o.reshape(*o.shape[:2], -1)

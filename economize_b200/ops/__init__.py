@@ -124,14 +124,19 @@ def attention(q: torch.Tensor, k_cache: torch.Tensor, v_cache: torch.Tensor, kv_
               q_offset: int = 0, k_scale: torch.Tensor | None = None,
               v_scale: torch.Tensor | None = None, keep: torch.Tensor | None = None,
               lse_out: torch.Tensor | None = None, kivi: torch.Tensor | None = None,
-              kivi_chunks: torch.Tensor | None = None, kivi_bits: int = 0) -> torch.Tensor:
+              kivi_chunks: torch.Tensor | None = None, kivi_bits: int = 0, tail: int = 0) -> torch.Tensor:
     """Causal / tree-masked attention over the slot cache (see :func:`.reference.attention`); fp8 caches take
     per-KV-head scales, ``keep`` (int32 bit words ``[B, H_kv, S / 32]``) hides evicted committed slots and
-    ``lse_out [B, T, H]`` receives every row's log2-domain log-sum-exp."""
+    ``lse_out [B, T, H]`` receives every row's log2-domain log-sum-exp.
+
+    ``tail > 0`` (passes of at most 64 queries) reduces the keys at the last ``tail`` positions before each query,
+    and its own new keys, one at a time in position order: a verification pass then computes every query bit for
+    bit as a one-token pass at the same position does, for trees up to ``tail`` deep (the CPU path computes the
+    same values without that rounding guarantee)."""
     scale = float(scale if scale is not None else q.shape[-1] ** -0.5)
     if q.is_cuda:
         return require().attention(q, k_cache, v_cache, kv_len, n_new, mask, scale, int(q_offset), None, k_scale,
-                                   v_scale, keep, lse_out, kivi, kivi_chunks, int(kivi_bits))
+                                   v_scale, keep, lse_out, kivi, kivi_chunks, int(kivi_bits), int(tail))
     return reference.attention(q, k_cache, v_cache, kv_len, n_new, mask, scale, q_offset=q_offset, k_scale=k_scale,
                                v_scale=v_scale, keep=keep, lse_out=lse_out, kivi=kivi, kivi_chunks=kivi_chunks,
                                kivi_bits=kivi_bits)

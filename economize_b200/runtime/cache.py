@@ -76,6 +76,9 @@ class StepBatch:
     q_offset: int = 0
     #: a prompt pass starting at slot 0 (KV eviction scores the prompt during it)
     is_prefill: bool = False
+    #: a pass over prompt tokens (a whole prefill or one chunk of a chunked prefill): attention reduces its keys by
+    #: slot, without the exact tail of decode passes, so a chunked prefill matches a whole one
+    prompt: bool = False
 
     @staticmethod
     def prefill(lengths: torch.Tensor, width: int) -> StepBatch:
@@ -84,4 +87,4 @@ class StepBatch:
         device = lengths.device
         positions = torch.arange(width, device=device, dtype=torch.int32).expand(batch, width).contiguous()
         return StepBatch(torch.zeros(batch, dtype=torch.int32, device=device), lengths.to(torch.int32), positions,
-                         is_prefill=True)
+                         is_prefill=True, prompt=True)

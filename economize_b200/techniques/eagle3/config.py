@@ -19,8 +19,16 @@ EAGLE3_HEADS = ("own", "shared")
 
 
 def default_aux_layers(num_layers: int) -> tuple[int, ...]:
-    """EAGLE-3's low, middle and high features: outputs of blocks ``(2, L // 2, L - 3)``, clamped, no repeats."""
-    return tuple(sorted({min(max(layer, 0), num_layers) for layer in (2, num_layers // 2, num_layers - 3)}))
+    """The block outputs EAGLE-3 fuses for an ``num_layers``-block model: one after block 2, one halfway and one three
+    blocks before the end. A shallow model keeps the distinct ones that exist (``0`` is the embedding output)."""
+    wanted = (2, num_layers // 2, num_layers - 3)
+    chosen: list[int] = []
+    for layer in wanted:
+        layer = num_layers if layer > num_layers else (0 if layer < 0 else layer)
+        if layer not in chosen:
+            chosen.append(layer)
+    chosen.sort()
+    return tuple(chosen)
 
 
 @dataclass(frozen=True)
@@ -43,16 +51,18 @@ class Eagle3Config(DraftLayerConfig):
     norm_before_residual: bool = False
 
     def __post_init__(self) -> None:
-        if self.aux_layers is not None:
-            layers = tuple(int(x) for x in self.aux_layers)
-            check_indices("aux_layers", layers, allow_empty=False)
-            object.__setattr__(self, "aux_layers", layers)
+        super().__post_init__()
         check_choice("head", self.head, EAGLE3_HEADS)
         if self.draft_vocab is not None:
+            if self.head == "shared":
+                raise ConfigError("a reduced draft vocabulary belongs to the drafter's own head; with head='shared' "
+                                  "leave draft_vocab unset")
             check_positive("draft_vocab", self.draft_vocab)
-            if self.head != "own":
-                raise ConfigError("draft_vocab needs head='own'")
-        super().__post_init__()
+        if self.aux_layers is None:
+            return
+        fused = tuple(int(index) for index in self.aux_layers)
+        check_indices("aux_layers", fused, allow_empty=False)
+        object.__setattr__(self, "aux_layers", fused)
 
     def layers(self, num_layers: int) -> tuple[int, ...]:
         return self.aux_layers if self.aux_layers is not None else default_aux_layers(num_layers)

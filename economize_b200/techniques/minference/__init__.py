@@ -92,7 +92,8 @@ class MInferencePrefill:
                 kv = torch.full((b,), start, dtype=torch.int32, device=tokens.device)
                 n = (lengths - start).clamp(0, end - start).to(torch.int32)
                 pos = torch.arange(start, end, device=tokens.device, dtype=torch.int32).expand(b, end - start)
-                h, a = model.forward_step(tokens[:, start:end], StepBatch(kv, n, pos.contiguous()), cache, capture)
+                h, a = model.forward_step(tokens[:, start:end], StepBatch(kv, n, pos.contiguous(), prompt=True), cache,
+                                          capture)
                 outs.append(h)
                 auxes.append(a)
         finally:

@@ -1,8 +1,10 @@
 """The engine on the CUDA path (bf16, sm_100a kernels).
 
-In bf16 a tree pass and a one-token pass sum the same keys in a different slot order, so exact token equality with
-plain decoding holds only up to rounding. The check is therefore per token: under a full causal recompute of
-prompt + generated tokens, every generated token is the argmax, or within a rounding-sized logit gap of it."""
+Greedy speculative decoding (chains and trees) must reproduce plain greedy decoding through the same engine token
+for token: the projections split K the same way for one row and for a verification pass, and attention takes the
+last positions before every query in position order (the exact tail), so an accepted token's logits are the bits a
+one-token pass computes. Plain decoding itself is checked against a full causal recompute up to a rounding-sized
+logit gap (a prompt-length pass reduces keys differently from a one-token pass)."""
 
 import pytest
 import torch
@@ -53,8 +55,10 @@ def test_spec_decoding_is_greedy(em, cuda, graphs, tree):
     cfg = (eco.DecodeConfig(cycle_length=7, draft_policy="dynamic_tree", draft_policy_options=TREE,
                             cuda_graphs=graphs) if tree else eco.DecodeConfig(cycle_length=5, cuda_graphs=graphs))
     spec = em.decode_batch(prompts, 40, decoding=cfg)
-    for p, s in zip(prompts, spec):
+    plain = em.decode_batch(prompts, 40, decoding=eco.DecodeConfig(cycle_length=1))
+    for p, s, q in zip(prompts, spec, plain):
         assert s.tokens.numel() == 40
+        assert torch.equal(s.tokens, q.tokens)
         _assert_greedy(em, p, s.tokens)
     assert eco.ops.require().status(0) == 0
 

@@ -1,5 +1,5 @@
 """Sequoia static trees and SpecExec search (economize ``tests/test_sequoia.py`` and ``tests/test_specexec.py``):
-the dynamic program against exhaustive search, the options' checks, acceptance recording, and lossless decoding on
+the best-first tree search against exhaustive search, the options' checks, acceptance recording, and lossless decoding on
 the CPU fp32 path (both policies must reproduce plain greedy decoding)."""
 
 import itertools
@@ -31,7 +31,7 @@ def _all_trees(nodes: int, depth: int, ranks: int):
 
 
 @pytest.mark.parametrize("nodes,depth", [(3, 2), (5, 3), (6, 2)])
-def test_dp_matches_exhaustive_search(nodes, depth):
+def test_best_first_matches_exhaustive_search(nodes, depth):
     rates = (0.5, 0.2, 0.1)
     best = max(expected_tokens(t, rates) for t in _all_trees(nodes, depth, 3))
     tree = sequoia_tree(rates, nodes, depth)
@@ -40,7 +40,7 @@ def test_dp_matches_exhaustive_search(nodes, depth):
     assert expected_tokens(tree, rates) == pytest.approx(best)
 
 
-def test_dp_per_depth_rates_and_gaps():
+def test_best_first_per_depth_rates_and_gaps():
     per_depth = ((0.9, 0.05), (0.2, 0.3))  # after the root: confident; below: the 2nd rank is the likelier one
     best = max(expected_tokens(t, per_depth) for t in _all_trees(4, 3, 2))
     assert sequoia_tree(per_depth, 4, 3).expected == pytest.approx(best)
@@ -68,14 +68,14 @@ def test_static_tree_and_profile():
 
 
 @pytest.mark.parametrize("options,match", [
-    ({}, "exactly one"),
-    ({"acceptance": RATES, "paths": [(0,)]}, "exactly one"),
-    ({"paths": [(0, 1)]}, "no parent"),
+    ({}, "needs a tree"),
+    ({"acceptance": RATES, "paths": [(0,)]}, "not both"),
+    ({"paths": [(0, 1)]}, "not in the tree"),
     ({"paths": [(0,)], "depth": 3}, "explicit"),
-    ({"acceptance": (0.7, 0.5)}, "sum to at most 1"),
-    ({"acceptance": RATES, "draft_latency": 0.1}, "needs verify_latency"),
+    ({"acceptance": (0.7, 0.5)}, "sum to at"),
+    ({"acceptance": RATES, "draft_latency": 0.1}, "next to verify_latency"),
     ({"acceptance": RATES, "total_tokens": 80}, "at most 63"),
-    ({"acceptance": RATES, "bogus": 1}, "no options"),
+    ({"acceptance": RATES, "bogus": 1}, "unknown sequoia option"),
 ])
 def test_sequoia_options_are_checked(options, match):
     with pytest.raises(ConfigError, match=match):
