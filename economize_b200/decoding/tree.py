@@ -49,28 +49,32 @@ class TreeOptions:
 
     @classmethod
     def from_options(cls, options: Mapping[str, object], cycle_length: int) -> TreeOptions:
-        unknown = sorted(set(options) - {"depth", "topk", "total_tokens"})
-        if unknown:
-            raise ConfigError(f"draft_policy 'dynamic_tree' has no options {unknown}; it takes depth, topk and "
-                              "total_tokens")
-        values: dict[str, object] = {"depth": max(cycle_length - 1, 1), "topk": DEFAULT_TOPK, **options}
-        if "total_tokens" not in values:
-            d, k = values["depth"], values["topk"]
-            values["total_tokens"] = (min(DEFAULT_TOTAL_TOKENS, cls(d, k, 1).candidates)
-                                      if is_positive_int(d) and is_positive_int(k) else DEFAULT_TOTAL_TOKENS)
-        for name, value in values.items():
+        """Parse the ``dynamic_tree`` options. ``depth`` defaults to ``cycle_length - 1`` and ``topk`` to EAGLE-2's
+        10; without ``total_tokens`` the tree verifies EAGLE-2's 60 nodes, or every candidate when a shallow search
+        produces fewer."""
+        allowed = ("depth", "topk", "total_tokens")
+        stray = [name for name in options if name not in allowed]
+        if stray:
+            raise ConfigError(f"unknown dynamic_tree option(s) {sorted(stray)} (known: {', '.join(allowed)})")
+        depth = options.get("depth", max(cycle_length - 1, 1))
+        topk = options.get("topk", DEFAULT_TOPK)
+        for name, value in (("depth", depth), ("topk", topk)):
             if not is_positive_int(value):
-                raise ConfigError(f"draft_policy 'dynamic_tree' needs a positive integer {name}, got {value!r}")
-        tree = cls(int(values["depth"]), int(values["topk"]), int(values["total_tokens"]))
-        if tree.total_tokens > tree.candidates:
-            raise ConfigError(f"total_tokens={tree.total_tokens} exceeds the {tree.candidates} candidates of a tree "
-                              f"of depth {tree.depth} and topk {tree.topk}")
-        if tree.total_tokens + 1 > MAX_TREE_NODES:
-            raise ConfigError(f"a verified tree holds at most {MAX_TREE_NODES - 1} draft nodes, got "
+                raise ConfigError(f"dynamic_tree's {name} must be a positive integer, not {value!r}")
+        pool = int(topk) + (int(depth) - 1) * int(topk) ** 2  # candidates the search ranks
+        total = options.get("total_tokens", min(DEFAULT_TOTAL_TOKENS, pool))
+        if not is_positive_int(total):
+            raise ConfigError(f"dynamic_tree's total_tokens must be a positive integer, not {total!r}")
+        tree = cls(int(depth), int(topk), int(total))
+        if tree.total_tokens > pool:
+            raise ConfigError(f"only {pool} candidates exist for depth {tree.depth} and topk {tree.topk}, fewer than "
                               f"total_tokens={tree.total_tokens}")
+        if tree.total_tokens >= MAX_TREE_NODES:
+            raise ConfigError(f"total_tokens={tree.total_tokens}: one verified pass holds at most "
+                              f"{MAX_TREE_NODES - 1} draft nodes next to the root")
         if tree.forwarded > MAX_TREE_NODES:
-            raise ConfigError(f"(depth - 1) * topk = {tree.forwarded} forwarded draft nodes exceed "
-                              f"{MAX_TREE_NODES}")
+            raise ConfigError(f"the search runs (depth - 1) x topk = {tree.forwarded} nodes through the drafter, "
+                              f"more than the {MAX_TREE_NODES} an ancestor word covers")
         return tree
 
 

@@ -13,9 +13,8 @@ allocation, and the weight and MLP objects that route decoding steps to the spar
 
 from __future__ import annotations
 
-import math
 from collections.abc import Callable, Mapping
-from dataclasses import dataclass, fields
+from dataclasses import dataclass
 
 import torch
 import torch.nn.functional as F
@@ -23,9 +22,8 @@ from torch import nn
 
 from ..errors import ConfigError
 from ..runtime.phase import current_phase
-from ..validation import check_choice
 
-__all__ = ["MAX_ROWS", "PREFILL_MODES", "GreedyStep", "PhasePolicy", "TealWeight", "TransposedWeight",
+__all__ = ["MAX_ROWS", "POLICY_PHASES", "PREFILL_MODES", "GreedyStep", "PhasePolicy", "TealWeight", "TransposedWeight",
            "apply_mode", "block_sparsity", "cats_mlp", "greedy_allocation", "greedy_error", "kept_channels",
            "kept_mlp", "magnitude_quantile", "sparsify", "topk_mask", "uniform_allocation"]
 
@@ -36,6 +34,10 @@ MAX_ROWS = 4
 #: How a forward call's tokens are treated: ``"dense"`` unchanged, ``"second_half"`` the last ``max(1, S // 2)``
 #: positions of every sequence are sparsified (TEAL's perplexity protocol), ``"all"`` every position.
 PREFILL_MODES = ("dense", "second_half", "all")
+
+
+#: The kinds of forward call a :class:`PhasePolicy` distinguishes (the engine's phases, plus calls outside it).
+POLICY_PHASES = ("prefill", "refresh", "decode", "draft", "outside")
 
 
 @dataclass(frozen=True)
@@ -52,37 +54,41 @@ class PhasePolicy:
     outside: str = "dense"
 
     def __post_init__(self) -> None:
-        for f in fields(self):
-            check_choice(f"PhasePolicy.{f.name}", getattr(self, f.name), PREFILL_MODES)
+        for phase in POLICY_PHASES:
+            mode = getattr(self, phase)
+            if mode not in PREFILL_MODES:
+                raise ConfigError(f"PhasePolicy.{phase}={mode!r} is not a mode; use one of {', '.join(PREFILL_MODES)}")
 
     @classmethod
     def from_prefill(cls, mode: str) -> PhasePolicy:
         """The policy of ``prefill=mode``: the exact passes and multi-token calls outside decoding follow ``mode``."""
-        return cls(prefill=mode, refresh=mode, outside=mode)
+        return cls(**{phase: mode for phase in ("prefill", "refresh", "outside")})
 
     @classmethod
     def coerce(cls, value) -> PhasePolicy:
-        if isinstance(value, PhasePolicy):
+        """A policy from itself, a mode name (:meth:`from_prefill`) or a mapping of phase to mode."""
+        if isinstance(value, cls):
             return value
         if isinstance(value, str):
-            if value not in PREFILL_MODES:
-                raise ConfigError(f"prefill must be one of {PREFILL_MODES} or a PhasePolicy, got {value!r}")
-            return cls.from_prefill(value)
+            if value in PREFILL_MODES:
+                return cls.from_prefill(value)
+            raise ConfigError(f"{value!r} names no mode; a prefill mode is one of {', '.join(PREFILL_MODES)}")
         if isinstance(value, Mapping):
-            unknown = set(value) - {f.name for f in fields(cls)}
-            if unknown:
-                raise ConfigError(f"unknown PhasePolicy fields {sorted(unknown)}")
-            return cls(**value)
-        raise ConfigError(f"prefill must be a mode string, a mapping or a PhasePolicy, got {value!r}")
+            extra = [key for key in value if key not in POLICY_PHASES]
+            if extra:
+                raise ConfigError(f"a phase policy maps the phases {', '.join(POLICY_PHASES)} to modes; "
+                                  f"{sorted(extra)} are not phases")
+            return cls(**dict(value))
+        raise ConfigError(f"cannot read a phase policy from {type(value).__name__} {value!r}")
 
     def to_dict(self) -> dict[str, str]:
-        return {f.name: getattr(self, f.name) for f in fields(self)}
+        return {phase: getattr(self, phase) for phase in POLICY_PHASES}
 
     def mode(self, phase: str | None, tokens: int | None) -> str:
         """The mode of a call in ``phase`` over ``tokens`` positions per sequence."""
-        if phase is None:
-            return self.decode if tokens == 1 else self.outside
-        return str(getattr(self, phase))
+        if phase is not None:
+            return str(getattr(self, phase))
+        return self.decode if tokens == 1 else self.outside
 
 
 def tokens_per_sequence(x: torch.Tensor) -> int | None:
@@ -126,16 +132,22 @@ def magnitude_quantile(sorted_magnitudes: torch.Tensor, q: float) -> float:
 
 def block_sparsity(sparsities: Mapping[str, float], sizes: Mapping[str, int]) -> float:
     """Parameter-weighted mean sparsity of a layer's maps: the fraction of its weight reads a sparse kernel skips."""
-    total = sum(sizes.values())
-    return sum(sparsities[n] * s for n, s in sizes.items()) / max(total, 1)
+    names = list(sizes)
+    weights = [sizes[n] for n in names]
+    skipped = sum(w * sparsities[n] for n, w in zip(names, weights))
+    return skipped / max(sum(weights), 1)
 
 
 def uniform_allocation(sizes: Mapping[str, int], target: float) -> dict[str, float]:
-    return dict.fromkeys(sizes, target)
+    """Every map of the layer at the same sparsity ``target``."""
+    return {name: target for name in sizes}
 
 
 @dataclass(frozen=True)
 class GreedyStep:
+    """One move of :func:`greedy_allocation`: the map that was raised, the layer's sparsity after the move and
+    the layer error the move measured."""
+
     name: str
     block_sparsity: float
     error: float
@@ -143,27 +155,35 @@ class GreedyStep:
 
 def greedy_allocation(error: Callable[[Mapping[str, float]], float], sizes: Mapping[str, int], target: float, *,
                       step: float = 0.05, unit: int | None = None) -> tuple[dict[str, float], list[GreedyStep]]:
-    """TEAL's block-wise greedy search (Algorithm 1 of Liu et al., 2025): from zero, repeatedly raise the sparsity
-    of the map whose move gives the lowest layer error, each map moving by ``step * unit / size`` so every move
-    adds the same to the layer-level sparsity, until that reaches ``target``."""
-    unit = unit or max(sizes.values())
-    steps = {n: step * unit / s for n, s in sizes.items()}
-    levels = dict.fromkeys(sizes, 0.0)
-    path: list[GreedyStep] = []
-    while block_sparsity(levels, sizes) < target - 1e-9:
-        best, best_err = None, math.inf
-        for n in sizes:
-            if levels[n] >= 1.0:
-                continue
-            trial = {**levels, n: min(1.0, levels[n] + steps[n])}
-            err = error(trial)
-            if err < best_err:
-                best, best_err = n, err
-        if best is None:
+    """TEAL's block-wise greedy allocation (Liu et al., 2025, Algorithm 1).
+
+    Every map's sparsity moves in increments sized so that one increment of any map adds ``step * unit / total``
+    to the layer's weighted sparsity (``unit``: the largest map's size by default). Each round evaluates ``error``
+    on every map raised by one increment and keeps the cheapest move; rounds continue until the layer reaches
+    ``target`` or no map can move. Returns the sparsities and the moves in order.
+    """
+    scale = unit if unit else max(sizes.values())
+    increment = {name: step * scale / size for name, size in sizes.items()}
+    count = {name: 0 for name in sizes}
+
+    def level(name: str, extra: int = 0) -> float:
+        return min(1.0, (count[name] + extra) * increment[name])
+
+    def levels(raise_one: str | None = None) -> dict[str, float]:
+        return {name: level(name, 1 if name == raise_one else 0) for name in sizes}
+
+    history: list[GreedyStep] = []
+    current = levels()
+    while block_sparsity(current, sizes) + 1e-9 < target:
+        movable = [name for name in sizes if level(name) < 1.0]
+        if not movable:
             break
-        levels[best] = min(1.0, levels[best] + steps[best])
-        path.append(GreedyStep(best, block_sparsity(levels, sizes), best_err))
-    return levels, path
+        trials = [(error(levels(name)), position, name) for position, name in enumerate(movable)]
+        cost, _, chosen = min(trials)
+        count[chosen] += 1
+        current = levels()
+        history.append(GreedyStep(chosen, block_sparsity(current, sizes), cost))
+    return current, history
 
 
 def greedy_error(reference: torch.Tensor, output: torch.Tensor, fraction: float = 0.25) -> float:
