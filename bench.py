@@ -668,8 +668,9 @@ def main() -> None:
     if hasattr(model, "refresh"):
         model.refresh()
     tpg = getattr(engine_model, "tp", None)
-    if tpg is not None and getattr(tpg, "comm", None) is not None:
-        tpg.comm.close()
+    for runtime in (getattr(tpg, "comm", None), getattr(tpg, "sp", None)):
+        if runtime is not None:
+            runtime.close()
     results.clear()
     del step, model
     import gc

@@ -1115,6 +1115,123 @@ void linear_push(Tensor x, Tensor w, std::vector<int64_t> ptrs, int64_t rank, in
   TORCH_CHECK(rc == 0, "linear_push: unsupported shape or launch failure");
 }
 
+// ---- sequence-parallel tensor parallelism (tp_sp.cu) ----------------------------------------------------------
+// A rank's buffer layout from (world, rank, hidden, max_rows, n_cap); returns its size in bytes.
+int64_t sp_buffer_bytes(int64_t world, int64_t rank, int64_t hidden, int64_t max_rows, int64_t n_cap) {
+  return ecz::sp_layout(world, rank, hidden, max_rows, n_cap).bytes;
+}
+
+ecz::SpLayout sp_check(const std::vector<int64_t>& ptrs, int64_t rank, int64_t hidden, int64_t max_rows,
+                       int64_t n_cap) {
+  TORCH_CHECK(!ptrs.empty() && rank >= 0 && rank < static_cast<int64_t>(ptrs.size()), "sp: bad rank or peers");
+  return ecz::sp_layout(static_cast<int>(ptrs.size()), static_cast<int>(rank), static_cast<int>(hidden),
+                        static_cast<int>(max_rows), static_cast<int>(n_cap));
+}
+
+// Reduce this rank's reduce-scatter partials (or, with partials = false, take resid alone), add the residual rows
+// [rows, H], RMSNorm with w and all-gather the normed rows at row0; returns the new residual rows.
+Tensor sp_reduce_norm(std::vector<int64_t> ptrs, int64_t rank, int64_t hidden, int64_t max_rows, int64_t n_cap,
+                      bool partials, Tensor resid, Tensor w, double eps, int64_t row0, int64_t cap_slot) {
+  CHECK_CUDA(w);
+  CHECK_BF16(w);
+  CHECK_BF16(resid);
+  const ecz::SpLayout L = sp_check(ptrs, rank, hidden, max_rows, n_cap);
+  c10::cuda::CUDAGuard guard(w.device());
+  resid = resid.contiguous();
+  TORCH_CHECK(resid.dim() == 2 && resid.size(1) == hidden && w.numel() == hidden, "sp_reduce_norm: resid [rows, H]");
+  if (resid.numel() > 0) CHECK_ON(resid, w);
+  auto out = at::empty_like(resid);
+  const int rc = ecz::launch_sp_reduce_norm(peer_ptrs(ptrs), L, partials, resid.numel() ? resid.data_ptr() : nullptr,
+                                            resid.numel() ? out.data_ptr() : nullptr, w.data_ptr(),
+                                            static_cast<int>(resid.size(0)), static_cast<int>(row0),
+                                            static_cast<float>(eps), static_cast<int>(cap_slot),
+                                            status_word(w.device()), at::cuda::getCurrentCUDAStream());
+  TORCH_CHECK(rc == 0, "sp_reduce_norm: rows, offset or capture slot outside the buffer");
+  return out;
+}
+
+// Wait for the current all-gather round and return its rows [rows, H].
+Tensor sp_fetch(std::vector<int64_t> ptrs, int64_t rank, int64_t hidden, int64_t max_rows, int64_t n_cap,
+                int64_t rows, Tensor like) {
+  const ecz::SpLayout L = sp_check(ptrs, rank, hidden, max_rows, n_cap);
+  c10::cuda::CUDAGuard guard(like.device());
+  auto out = at::empty({rows, hidden}, like.options().dtype(at::kBFloat16));
+  const int rc = ecz::launch_sp_fetch(peer_ptrs(ptrs), L, out.data_ptr(), static_cast<int>(rows),
+                                      status_word(like.device()), at::cuda::getCurrentCUDAStream());
+  TORCH_CHECK(rc == 0, "sp_fetch: rows outside the buffer");
+  return out;
+}
+
+// Captured residual rows [rows, H] of capture slot `slot` (valid once a later all-gather round was consumed).
+Tensor sp_capture(std::vector<int64_t> ptrs, int64_t rank, int64_t hidden, int64_t max_rows, int64_t n_cap,
+                  int64_t slot, int64_t rows, Tensor like) {
+  const ecz::SpLayout L = sp_check(ptrs, rank, hidden, max_rows, n_cap);
+  TORCH_CHECK(slot >= 0 && slot < n_cap && rows <= max_rows, "sp_capture: slot or rows outside the buffer");
+  c10::cuda::CUDAGuard guard(like.device());
+  auto out = at::empty({rows, hidden}, like.options().dtype(at::kBFloat16));
+  const char* src = reinterpret_cast<const char*>(ptrs[rank]) + L.cap_off + slot * max_rows * hidden * 2;
+  TORCH_CHECK(cudaMemcpyAsync(out.data_ptr(), src, rows * hidden * 2, cudaMemcpyDeviceToDevice,
+                              at::cuda::getCurrentCUDAStream()) == cudaSuccess, "sp_capture: copy failed");
+  return out;
+}
+
+// All-gather -> GEMM: y [rows, N] = X . w^T with X the current all-gather round's rows (the GEMM waits for them).
+Tensor sp_linear_ag(std::vector<int64_t> ptrs, int64_t rank, int64_t hidden, int64_t max_rows, int64_t n_cap,
+                    int64_t rows, Tensor w) {
+  CHECK_CUDA(w);
+  CHECK_BF16(w);
+  const ecz::SpLayout L = sp_check(ptrs, rank, hidden, max_rows, n_cap);
+  TORCH_CHECK(w.dim() == 2 && w.size(1) == hidden && rows >= 1 && rows <= max_rows, "sp_linear_ag: w [N, H]");
+  c10::cuda::CUDAGuard guard(w.device());
+  w = w.contiguous();
+  const int M = static_cast<int>(rows), K = static_cast<int>(hidden), N = static_cast<int>(w.size(0));
+  auto y = at::empty({M, N}, w.options());
+  const char* ag = reinterpret_cast<const char*>(ptrs[rank]) + L.ag_off;
+  const int bn = ecz::gemm_block_n(M);
+  const CUtensorMap* tw = tensor_map(w.data_ptr(), N, K, K, 128);
+  const CUtensorMap* tx0 = tensor_map(ag, M, K, K, bn);
+  const CUtensorMap* tx1 = tensor_map(ag + static_cast<size_t>(max_rows) * hidden * 2, M, K, K, bn);
+  ecz::AgWait wait;
+  wait.ctrl = reinterpret_cast<unsigned*>(ptrs[rank]);
+  wait.world = static_cast<int>(ptrs.size());
+  const int sms = num_sms(w.get_device());
+  const int rc = ecz::launch_gemm_cluster(tw, tx0, y.data_ptr(), M, N, K, ecz::gemm_cluster_splits(M, N, K, sms),
+                                          status_word(w.device()), at::cuda::getCurrentCUDAStream(), nullptr, &wait,
+                                          tx1);
+  TORCH_CHECK(rc == 0, "sp_linear_ag: unsupported shape or launch failure");
+  return y;
+}
+
+// GEMM -> reduce-scatter: x [rows, K] . w^T with every output row stored into its owner rank's partial slot.
+void sp_linear_rs(std::vector<int64_t> ptrs, int64_t rank, int64_t hidden, int64_t max_rows, int64_t n_cap,
+                  Tensor x, Tensor w) {
+  CHECK_CUDA(x);
+  CHECK_BF16(x);
+  CHECK_BF16(w);
+  const ecz::SpLayout L = sp_check(ptrs, rank, hidden, max_rows, n_cap);
+  TORCH_CHECK(x.dim() == 2 && w.dim() == 2 && x.size(1) == w.size(1) && w.size(0) == hidden,
+              "sp_linear_rs expects x [M, K] and w [H, K]");
+  TORCH_CHECK(x.size(0) >= 1 && x.size(0) <= max_rows, "sp_linear_rs: more rows than the buffer holds");
+  c10::cuda::CUDAGuard guard(x.device());
+  x = x.contiguous();
+  w = w.contiguous();
+  const int M = static_cast<int>(x.size(0)), K = static_cast<int>(x.size(1)), N = static_cast<int>(hidden);
+  ecz::PeerOut peer{};
+  peer.ptrs = peer_ptrs(ptrs);
+  peer.world = L.world;
+  peer.rank = L.rank;
+  peer.mode = 1;
+  peer.shard_rows = (M + L.world - 1) / L.world;
+  peer.shard_max = L.shard_max;
+  peer.data_off = L.rs_off;
+  const CUtensorMap* tw = tensor_map(w.data_ptr(), N, K, K, 128);
+  const CUtensorMap* tx = tensor_map(x.data_ptr(), M, K, K, ecz::gemm_block_n(M));
+  const int sms = num_sms(x.get_device());
+  const int rc = ecz::launch_gemm_cluster(tw, tx, nullptr, M, N, K, ecz::gemm_cluster_splits(M, N, K, sms),
+                                          status_word(x.device()), at::cuda::getCurrentCUDAStream(), &peer);
+  TORCH_CHECK(rc == 0, "sp_linear_rs: unsupported shape or launch failure");
+}
+
 void push(Tensor src, std::vector<int64_t> ptrs, int64_t rank, int64_t parity, int64_t slot_elems) {
   CHECK_CUDA(src);
   CHECK_BF16(src);
@@ -1256,6 +1373,12 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("symm_control_bytes", &symm_control_bytes, "bytes of the control block before the data slots");
   m.def("push", &push, "store this rank's partial into every peer's slot and signal arrival");
   m.def("linear_push", &linear_push, "row-parallel GEMM whose output tiles go into every peer's slot");
+  m.def("sp_buffer_bytes", &sp_buffer_bytes, "bytes of one rank's sequence-parallel buffer");
+  m.def("sp_reduce_norm", &sp_reduce_norm, "reduce-scatter partials + residual + RMSNorm, all-gather the rows");
+  m.def("sp_fetch", &sp_fetch, "wait for the current all-gather round and copy its rows");
+  m.def("sp_capture", &sp_capture, "copy the captured residual rows of a capture slot");
+  m.def("sp_linear_ag", &sp_linear_ag, "all-gather -> GEMM (the GEMM waits for every rank's rows)");
+  m.def("sp_linear_rs", &sp_linear_rs, "GEMM -> reduce-scatter (rows stored into their owner's partial slot)");
   m.def("reduce_rmsnorm", &reduce_rmsnorm, "wait for every rank's partial, sum, add residual, RMSNorm");
   m.def("status", &status, "read and clear the device status word of bounded waits");
   m.def("attention_plan", &attention_plan, "(m_tiles, splits, chunks_per_split) of an attention launch");

@@ -47,19 +47,64 @@ __device__ __forceinline__ bf16* peer_slot(const PeerOut& peer, int p) {
          (static_cast<long>(peer.parity) * peer.world + peer.rank) * peer.slot_elems;
 }
 
-__device__ __forceinline__ void push_signal(const PeerOut& peer, bool wrote, unsigned writers_total) {
+__device__ __forceinline__ void push_signal(const PeerOut& peer, bool wrote, unsigned writers_total, int parity) {
   // every CTA that stored a tile counts itself; the last one signals the peers (writers_total = tiles). The CTA
   // barrier orders all threads' stores before thread 0's system-scope fence.
   __syncthreads();
   if (threadIdx.x == 0 && wrote) {
     __threadfence_system();
     unsigned* own = reinterpret_cast<unsigned*>(peer.ptrs.ptr[peer.rank]);
-    const unsigned done = atomicAdd(own + 4, 1u);  // push_done of the control block
+    const unsigned done = atomicAdd(own + kSpPushDone, 1u);  // push_done of the control block
     if (done == writers_total - 1) {
-      own[4] = 0;
+      own[kSpPushDone] = 0;
       __threadfence_system();
-      for (int p = 0; p < peer.world; ++p) atomicAdd_system(static_cast<unsigned*>(peer.ptrs.ptr[p]) + peer.parity, 1u);
+      for (int p = 0; p < peer.world; ++p)
+        atomicAdd_system(static_cast<unsigned*>(peer.ptrs.ptr[p]) + kSpRsArrive + parity, 1u);
     }
+  }
+}
+
+// Mode-1 (reduce-scatter) destination of output element (m, n): the owner rank's partial slot of this rank.
+__device__ __forceinline__ bf16* scatter_dst(const PeerOut& peer, int parity, int m, int n, int N) {
+  const int owner = m / peer.shard_rows;
+  const int local = m - owner * peer.shard_rows;
+  bf16* base = reinterpret_cast<bf16*>(static_cast<uint8_t*>(peer.ptrs.ptr[owner]) + peer.data_off);
+  return base + ((static_cast<size_t>(parity) * peer.world + peer.rank) * peer.shard_max + local) *
+                    static_cast<size_t>(N) + n;
+}
+
+__device__ __forceinline__ unsigned ld_acquire_sys_u32(const unsigned* p) {
+  unsigned v;
+  asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+
+// The all-gather wait of an AG -> GEMM consumer (one thread): returns the round's parity. On timeout the status
+// records kStatusWaitPeer and the GEMM proceeds on whatever the buffer holds (its copies then complete normally).
+__device__ __forceinline__ int ag_wait(const AgWait& ag, unsigned* status) {
+  const int par = static_cast<int>(ag.ctrl[kSpAgRound] & 1u);
+  const unsigned* flag = ag.ctrl + kSpAgArrive + par;
+  if (ld_acquire_sys_u32(flag) < static_cast<unsigned>(ag.world)) {
+    const unsigned long long start = global_timer_ns();
+    while (ld_acquire_sys_u32(flag) < static_cast<unsigned>(ag.world)) {
+      if (global_timer_ns() - start > kWaitLimitNs) {
+        atomicOr(status, kStatusWaitPeer);
+        break;
+      }
+    }
+  }
+  asm volatile("fence.proxy.async.global;" ::: "memory");  // the peers' stores become visible to TMA reads
+  return par;
+}
+
+// The last CTA of an AG -> GEMM consumer resets the round's arrival count and advances the round.
+__device__ __forceinline__ void ag_release(const AgWait& ag, int par, unsigned ctas) {
+  __threadfence();
+  if (atomicAdd(ag.ctrl + kSpAgDone, 1u) == ctas - 1) {
+    ag.ctrl[kSpAgDone] = 0;
+    ag.ctrl[kSpAgArrive + par] = 0;
+    ag.ctrl[kSpAgRound] += 1u;
+    __threadfence();
   }
 }
 
@@ -246,7 +291,7 @@ __global__ void __launch_bounds__(128, OCC)
     }
     wrote = last;
   }
-  if (peer.world > 0 && ok) push_signal(peer, wrote, gridDim.x * gridDim.y);
+  if (peer.world > 0 && ok) push_signal(peer, wrote, gridDim.x * gridDim.y, peer.parity);
 }
 
 __global__ void __launch_bounds__(256) splitk_reduce_kernel(const float* __restrict__ ws, bf16* __restrict__ y,
@@ -310,7 +355,8 @@ int run_gemm(const CUtensorMap& tm_w, const CUtensorMap& tm_x, void* y, float* w
 template <int BN>
 __global__ void __launch_bounds__(128, split_occupancy<BN>())
     gemm_cluster_kernel(const __grid_constant__ CUtensorMap tm_w, const __grid_constant__ CUtensorMap tm_x,
-                        bf16* __restrict__ y, int M, int N, int K, int kb_per_split, unsigned* status, PeerOut peer) {
+                        bf16* __restrict__ y, int M, int N, int K, int kb_per_split, unsigned* status, PeerOut peer,
+                        AgWait ag, const __grid_constant__ CUtensorMap tm_x1) {
   using Cfg = GemmCfg<BN, split_occupancy<BN>()>;
   constexpr int S = Cfg::kStages;
   static_assert(BN * kBM * 4 <= S * Cfg::kStageBytes, "the partial tile must fit the stage ring");
@@ -352,6 +398,7 @@ __global__ void __launch_bounds__(128, split_occupancy<BN>())
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
 
+  int ag_par = 0;
   if (nkb > 0 && warp == 0 && lane == 0) {
     const int pre = nkb < S ? nkb : S;
     for (int kb = 0; kb < pre; ++kb) {  // weights first: they do not depend on the previous kernel
@@ -359,7 +406,9 @@ __global__ void __launch_bounds__(128, split_occupancy<BN>())
       tma_load_2d(a_tiles + kb * kABytes, &tm_w, &full[kb], (kb0 + kb) * kBK, n0);
     }
     pdl_wait();
-    for (int kb = 0; kb < pre; ++kb) tma_load_2d(b_tiles + kb * Cfg::kBBytes, &tm_x, &full[kb], (kb0 + kb) * kBK, m0);
+    if (ag.ctrl != nullptr) ag_par = ag_wait(ag, status);  // all-gather -> GEMM: the rows of every rank arrived
+    const CUtensorMap* mx = ag_par ? &tm_x1 : &tm_x;
+    for (int kb = 0; kb < pre; ++kb) tma_load_2d(b_tiles + kb * Cfg::kBBytes, mx, &full[kb], (kb0 + kb) * kBK, m0);
     for (int kb = pre; kb < nkb; ++kb) {
       const int s = kb % S;
       const uint32_t use = kb / S;
@@ -367,7 +416,7 @@ __global__ void __launch_bounds__(128, split_occupancy<BN>())
       mbar_arrive_expect_tx(&full[s], Cfg::kStageBytes);
       const int kx = (kb0 + kb) * kBK;
       tma_load_2d(a_tiles + s * kABytes, &tm_w, &full[s], kx, n0);
-      tma_load_2d(b_tiles + s * Cfg::kBBytes, &tm_x, &full[s], kx, m0);
+      tma_load_2d(b_tiles + s * Cfg::kBBytes, mx, &full[s], kx, m0);
     }
   } else if (nkb > 0 && warp == 1 && lane == 0) {
     constexpr uint32_t idesc = idesc_bf16_f32(kBM, BN);
@@ -394,6 +443,9 @@ __global__ void __launch_bounds__(128, split_occupancy<BN>())
   const bool ok = nkb > 0 && !*abort_flag;
   const uint32_t lane_base = tmem + (static_cast<uint32_t>(warp * 32) << 16);
   const int feat = warp * 32 + lane;  // this thread's TMEM lane = output feature n0 + feat
+  // reduce-scatter round parity: this rank's own round counter (its predecessor grids have completed)
+  const int rs_par = peer.mode == 1 ? static_cast<int>(static_cast<const unsigned*>(peer.ptrs.ptr[peer.rank])[kSpRsRound] & 1u)
+                                    : peer.parity;
   if (splits == 1) {
     if (ok) {
 #pragma unroll 1
@@ -408,6 +460,7 @@ __global__ void __launch_bounds__(128, split_occupancy<BN>())
             if (m >= M) continue;
             const bf16 o = __float2bfloat16(v[j]);
             if (peer.world == 0) y[static_cast<size_t>(m) * N + n] = o;
+            else if (peer.mode == 1) *scatter_dst(peer, rs_par, m, n, N) = o;
             else for (int p = 0; p < peer.world; ++p) peer_slot(peer, p)[static_cast<size_t>(m) * N + n] = o;
           }
         }
@@ -445,6 +498,8 @@ __global__ void __launch_bounds__(128, split_occupancy<BN>())
         packed.y = *reinterpret_cast<uint32_t*>(&hi);
         if (peer.world == 0) {
           *reinterpret_cast<uint2*>(y + static_cast<size_t>(m) * N + n) = packed;
+        } else if (peer.mode == 1) {
+          *reinterpret_cast<uint2*>(scatter_dst(peer, rs_par, m, n, N)) = packed;
         } else {
           for (int p = 0; p < peer.world; ++p)
             *reinterpret_cast<uint2*>(peer_slot(peer, p) + static_cast<size_t>(m) * N + n) = packed;
@@ -456,12 +511,19 @@ __global__ void __launch_bounds__(128, split_occupancy<BN>())
   tc_fence_before();
   __syncthreads();
   if (warp == 0) tmem_dealloc(tmem, Cfg::kTmemCols);
-  if (peer.world > 0 && ok) push_signal(peer, true, gridDim.x * gridDim.y * gridDim.z);
+  if (peer.world > 0 && ok) push_signal(peer, true, gridDim.x * gridDim.y * gridDim.z, rs_par);
+  if (ag.ctrl != nullptr && threadIdx.x == 0) {
+    // every CTA's producer has waited (it is this thread): the last one closes the round. ag_par was set by this
+    // thread's wait; CTAs without K work read the round's parity themselves.
+    const int par = nkb > 0 ? ag_par : static_cast<int>(ag.ctrl[kSpAgRound] & 1u);
+    ag_release(ag, par, gridDim.x * gridDim.y * gridDim.z);
+  }
 }
 
 template <int BN>
 int run_gemm_cluster(const CUtensorMap& tm_w, const CUtensorMap& tm_x, void* y, int M, int N, int K, int splits,
-                     unsigned* status, cudaStream_t stream, const PeerOut& peer) {
+                     unsigned* status, cudaStream_t stream, const PeerOut& peer, const AgWait& ag,
+                     const CUtensorMap& tm_x1) {
   using Cfg = GemmCfg<BN, split_occupancy<BN>()>;
   set_max_smem(gemm_cluster_kernel<BN>, Cfg::kSmem);
   const int total_kb = (K + kBK - 1) / kBK;
@@ -482,7 +544,7 @@ int run_gemm_cluster(const CUtensorMap& tm_w, const CUtensorMap& tm_x, void* y, 
   cfg.attrs = attr;
   cfg.numAttrs = 2;
   const cudaError_t err = cudaLaunchKernelEx(&cfg, gemm_cluster_kernel<BN>, tm_w, tm_x, static_cast<bf16*>(y), M, N,
-                                             K, kbps, status, peer);
+                                             K, kbps, status, peer, ag, tm_x1);
   return err == cudaSuccess ? 0 : -2;
 }
 
@@ -792,15 +854,21 @@ int gemm_cluster_capacity(int M, int splits) {
 }
 
 int launch_gemm_cluster(const CUtensorMap* tm_w, const CUtensorMap* tm_x, void* y, int M, int N, int K, int splits,
-                        unsigned* status, cudaStream_t stream, const PeerOut* peer) {
+                        unsigned* status, cudaStream_t stream, const PeerOut* peer, const AgWait* ag,
+                        const CUtensorMap* tm_x1) {
   if (K % 8 != 0 || N % 4 != 0 || splits < 1 || splits > 8) return -1;
   const PeerOut none{};
   const PeerOut& pe = peer != nullptr ? *peer : none;
+  if (pe.mode == 1 && (pe.shard_rows < 1 || pe.shard_max < pe.shard_rows || pe.world < 1 ||
+                       (M + pe.shard_rows - 1) / pe.shard_rows > pe.world)) return -1;
+  const AgWait no_wait{};
+  const AgWait& aw = ag != nullptr ? *ag : no_wait;
+  const CUtensorMap& x1 = tm_x1 != nullptr ? *tm_x1 : *tm_x;
   switch (gemm_block_n(M)) {
-    case 32: return run_gemm_cluster<32>(*tm_w, *tm_x, y, M, N, K, splits, status, stream, pe);
-    case 64: return run_gemm_cluster<64>(*tm_w, *tm_x, y, M, N, K, splits, status, stream, pe);
-    case 128: return run_gemm_cluster<128>(*tm_w, *tm_x, y, M, N, K, splits, status, stream, pe);
-    default: return run_gemm_cluster<256>(*tm_w, *tm_x, y, M, N, K, splits, status, stream, pe);
+    case 32: return run_gemm_cluster<32>(*tm_w, *tm_x, y, M, N, K, splits, status, stream, pe, aw, x1);
+    case 64: return run_gemm_cluster<64>(*tm_w, *tm_x, y, M, N, K, splits, status, stream, pe, aw, x1);
+    case 128: return run_gemm_cluster<128>(*tm_w, *tm_x, y, M, N, K, splits, status, stream, pe, aw, x1);
+    default: return run_gemm_cluster<256>(*tm_w, *tm_x, y, M, N, K, splits, status, stream, pe, aw, x1);
   }
 }
 

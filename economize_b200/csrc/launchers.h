@@ -13,6 +13,10 @@ struct PeerPtrs {
 };
 
 // Where a row-parallel GEMM pushes its output in tensor-parallel push mode (world == 0: ordinary output).
+//   mode 0 (all-reduce push): every output element goes into slot `rank` of every peer's buffer (parity `parity`).
+//   mode 1 (reduce-scatter, sequence-parallel buffers of tp_sp.cu): output row m goes only to its owner rank
+//   m / shard_rows, into that rank's partial slot [parity][rank][m % shard_rows]; the parity is the device-side round
+//   counter of this rank's own control block (read after the predecessor grid completed).
 struct PeerOut {
   PeerPtrs ptrs;
   int world = 0;
@@ -20,6 +24,29 @@ struct PeerOut {
   int parity = 0;
   long slot_elems = 0;
   long control_bytes = 256;
+  int mode = 0;
+  int shard_rows = 0;   // mode 1: tokens per rank (the last ranks may own fewer or none)
+  int shard_max = 0;    // mode 1: rows of one partial slot
+  long data_off = 0;    // mode 1: byte offset of the partial slots in every peer's buffer
+};
+
+// Control words (unsigned) at the start of a sequence-parallel buffer (tp_sp.cu). Rounds of each kind alternate
+// between two parities; the round counters live on the device so captured CUDA graphs replay with the right ones.
+constexpr int kSpRsArrive = 0;     // [2] source ranks whose reduce-scatter partials of a round arrived here
+constexpr int kSpPushDone = 4;     // CTAs of this rank's current reduce-scatter GEMM that finished
+constexpr int kSpReduceDone = 5;   // CTAs of this rank's current reduce kernel that finished
+constexpr int kSpRsRound = 6;      // reduce-scatter rounds this rank has consumed
+constexpr int kSpAgArrive = 8;     // [2] source ranks whose all-gather rows of a round arrived here
+constexpr int kSpAgDone = 10;      // CTAs of this rank's current all-gather consumer that finished waiting
+constexpr int kSpAgRound = 11;     // all-gather rounds this rank has consumed
+constexpr int kSpControlBytes = 256;
+
+// An all-gather -> GEMM consumer: the TMA producer of every CTA waits (bounded) until all `world` ranks' rows of the
+// current all-gather round arrived in this rank's buffer, then loads X from the round's parity (tensor map 0 or 1);
+// the last CTA resets the arrival count and advances the round. ctrl == nullptr: an ordinary GEMM.
+struct AgWait {
+  unsigned* ctrl = nullptr;
+  int world = 0;
 };
 
 struct AttnPlan {
@@ -64,7 +91,8 @@ int launch_gemm_bf16(const CUtensorMap* tm_w, const CUtensorMap* tm_x, void* y, 
 int gemm_cluster_splits(int M, int N, int K, int num_sms);
 int gemm_cluster_capacity(int M, int splits);
 int launch_gemm_cluster(const CUtensorMap* tm_w, const CUtensorMap* tm_x, void* y, int M, int N, int K, int splits,
-                        unsigned* status, cudaStream_t stream, const PeerOut* peer = nullptr);
+                        unsigned* status, cudaStream_t stream, const PeerOut* peer = nullptr,
+                        const AgWait* ag = nullptr, const CUtensorMap* tm_x1 = nullptr);
 
 // Persistent stream-K GEMM: `ws` holds gemm_persistent_ws_floats() floats, `counters` >= num_sms zeroed ints
 // private to the stream (the kernel resets them).
@@ -109,6 +137,21 @@ int launch_ngram(const int64_t* history, const int* len, int64_t* drafts, int B,
 
 // comm.cu: fused NVLink all-reduce (+ residual add + RMSNorm) on IPC-mapped symmetric buffers
 size_t symm_control_bytes();
+// tp_sp.cu: sequence-parallel tensor parallelism. `layout` describes one rank's buffer (see tp_sp.cu).
+struct SpLayout {
+  int world = 0, rank = 0, hidden = 0, max_rows = 0, shard_max = 0, n_cap = 0;
+  long rs_off = 0, ag_off = 0, cap_off = 0, bytes = 0;
+};
+SpLayout sp_layout(int world, int rank, int hidden, int max_rows, int n_cap);
+// Sum this rank's reduce-scatter partials (partials = true) of rows [row0, row0 + rows) in rank order, add the
+// residual shard, write the new residual, RMSNorm, and push the normed rows (and, with cap_slot >= 0, the residual
+// rows) into every rank's all-gather buffer; then signal the round. rows may be 0 (a rank that owns no token).
+int launch_sp_reduce_norm(const PeerPtrs& peers, const SpLayout& L, bool partials, const void* resid_in,
+                          void* resid_out, const void* w, int rows, int row0, float eps, int cap_slot,
+                          unsigned* status, cudaStream_t stream);
+// Wait for the current all-gather round and copy its rows [0, rows) into out (an all-gather consumer).
+int launch_sp_fetch(const PeerPtrs& peers, const SpLayout& L, void* out, int rows, unsigned* status,
+                    cudaStream_t stream);
 int launch_push(const void* src, long elems, const PeerPtrs& peers, int rank, int world, int parity, long slot_elems,
                 int num_sms, cudaStream_t stream);
 int launch_reduce_rmsnorm(const PeerPtrs& peers, int rank, int world, int parity, long slot_elems, const void* resid,

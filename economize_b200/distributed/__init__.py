@@ -29,18 +29,19 @@ def init_distributed(backend: str | None = None, timeout_s: float = 300.0) -> TP
     return TPGroup(dist.get_rank(), dist.get_world_size(), None)
 
 
-def tensor_parallel(model, tp: TPGroup | None = None, fused: bool = False):
+def tensor_parallel(model, tp: TPGroup | None = None, fused: bool = False, max_rows: int = 4096):
     """Shard an engine model (or the engine model of an :class:`~economize_b200.EfficientModel`) over ``tp``
-    (default: all ranks). With ``fused`` the row-parallel all-reduces run through the NVLink push/reduce kernels."""
+    (default: all ranks). With ``fused`` passes of up to ``max_rows`` tokens run sequence-parallel on the fused
+    GEMM -> reduce-scatter and all-gather -> GEMM kernels (NVLink peer stores); longer ones take NCCL."""
     from ..core.model import EfficientModel
 
     target = model.model if isinstance(model, EfficientModel) else model
     tp = tp or TPGroup(dist.get_rank(), dist.get_world_size(), None)
     if fused and tp.size > 1:
-        from ..parallel.comm import FusedAllReduce
+        from ..parallel.sp import SequenceParallel
 
         tp.fused = True
-        tp.comm = FusedAllReduce(tp, target.config.hidden_size)
+        tp.sp = SequenceParallel(tp, target.config.hidden_size, max_rows=max_rows)
     shard_model(target, tp)
     if isinstance(model, EfficientModel):
         model.refresh()

@@ -23,6 +23,7 @@ import torch
 from torch import nn
 
 from .. import ops
+from ..errors import ConfigError
 from ..runtime.cache import KVCache, StepBatch
 from .config import ModelConfig, rope_inv_freq
 
@@ -147,6 +148,8 @@ class CausalLM(nn.Module):
         if sparse is not None and not sparse.active and hidden is None and layers is None and \
                 sparse.covers(tokens, batch):
             return sparse.chunked_forward(self, tokens, batch, cache, capture)
+        if self._sequence_parallel(tokens, layers, hidden):
+            return self._forward_sp(tokens, batch, cache, capture)
         cos, sin = self.rope_tables()
         h = self.embed_tokens(tokens) if hidden is None else hidden
         resid: torch.Tensor | None = None
@@ -187,6 +190,59 @@ class CausalLM(nn.Module):
             aux[-2] = resid
         return out, aux
 
+    # ---- sequence-parallel tensor parallelism ------------------------------------------------------------------
+    def _sequence_parallel(self, tokens: torch.Tensor, layers, hidden) -> bool:
+        """Whether a pass runs on the fused reduce-scatter / all-gather kernels (parallel/sp.py): a whole-model pass
+        of a dense model without per-token layer policies, views that skip sublayers, or calibration hooks."""
+        tp = self.tp
+        sp = getattr(tp, "sp", None) if tp is not None else None
+        if sp is None or layers is not None or hidden is not None or not sp.fits(tokens.numel()):
+            return False
+        if self.config.is_moe or self.observer is not None or self.depth_policy is not None:
+            return False
+        return not any(getattr(layer, name, None) for layer in self.layers
+                       for name in ("skip_attn", "skip_mlp", "mlp_rule", "attn_input_hook"))
+
+    def _forward_sp(self, tokens: torch.Tensor, batch: StepBatch, cache: KVCache, capture: tuple[int, ...]):
+        """:meth:`forward_step` with the residual stream split by token between the sublayers: every sublayer is
+        an all-gather -> GEMM, this rank's heads or features, and a GEMM -> reduce-scatter whose owner adds the
+        residual, applies the next RMSNorm and all-gathers the result."""
+        c, sp = self.config, self.tp.sp
+        eps = c.rms_norm_eps
+        B, T = tokens.shape
+        M = B * T
+        cos, sin = self.rope_tables()
+        emb = self.embed_tokens(tokens)
+        lo, n = sp.shard(M)
+        resid = emb.reshape(M, -1)[lo:lo + n].contiguous()
+        wanted = sorted({i for i in capture if 0 < i <= c.num_layers} | ({c.num_layers} if -2 in capture else set()))
+        if len(wanted) > sp.n_cap:
+            raise ConfigError(f"{len(wanted)} captured block outputs exceed the {sp.n_cap} capture slots")
+        slot_of = {layer: slot for slot, layer in enumerate(wanted)}
+        resid = sp.reduce_norm(resid, self.layers[0].attn_norm, eps, M, partials=False)
+        for i, layer in enumerate(self.layers):
+            qkv = sp.ag_linear(layer.wqkv, M)
+            if layer.bqkv is not None:
+                qkv = qkv + layer.bqkv
+            o = self._attend(layer, i, qkv.reshape(B, T, -1), batch, cache, cos, sin)
+            sp.rs_linear(o, layer.wo)
+            resid = sp.reduce_norm(resid, layer.mlp_norm, eps, M)
+            a = ops.silu_mul(sp.ag_linear(layer.w_gate_up, M))
+            sp.rs_linear(a, layer.w_down)
+            nxt = self.layers[i + 1].attn_norm if i + 1 < len(self.layers) else self.norm
+            resid = sp.reduce_norm(resid, nxt, eps, M, capture=slot_of.get(i + 1, -1))
+        out = sp.fetch(M, emb).reshape(B, T, -1)
+        aux: dict[int, torch.Tensor] = {}
+        if 0 in capture:
+            aux[0] = emb
+        for layer_index, slot in slot_of.items():  # valid now: the fetch consumed the pass's last round
+            aux[layer_index] = sp.captured(slot, M, emb).reshape(B, T, -1)
+        if -1 in capture:
+            aux[-1] = out
+        if -2 in capture:
+            aux[-2] = aux[c.num_layers]
+        return out, aux
+
     def _materialize(self, h, partial: bool) -> torch.Tensor:
         """A branch output as a plain tensor: split-K partials summed, a row-parallel partial all-reduced."""
         if isinstance(h, ops.Partials):
@@ -223,6 +279,16 @@ class CausalLM(nn.Module):
         if hook is not None:
             hook(x)
         qkv = self._linear(x, layer.wqkv) if layer.bqkv is None else ops.linear(x, layer.wqkv, layer.bqkv)
+        o = self._attend(layer, index, qkv, batch, cache, cos, sin)
+        if self.observer is not None:
+            self.observer(index, "wo", o)
+        return self._row_linear(o, layer.wo)
+
+    def _attend(self, layer: DecoderLayer, index: int, qkv, batch: StepBatch, cache: KVCache, cos: torch.Tensor,
+                sin: torch.Tensor) -> torch.Tensor:
+        """Rotary embedding + KV-cache write of a QKV projection and the attention over the cache: the heads'
+        outputs ``[B, T, H_q * D]`` (this rank's heads under tensor parallelism)."""
+        c = self.config
         k_cache, v_cache = cache.layer(index)
         k_scale, v_scale = cache.layer_scales(index)
         q = ops.rope_store(qkv, batch.positions, cos, sin, self.local["num_heads"], self.local["num_kv_heads"],
@@ -242,10 +308,7 @@ class CausalLM(nn.Module):
                           k_scale=k_scale, v_scale=v_scale, keep=keep, tail=tail, **kivi)
         if self.kv_evictor is not None and batch.is_prefill:
             self.kv_evictor.observe_prefill(index, q, k_cache, v_cache, batch)
-        o = o.reshape(*o.shape[:2], -1)
-        if self.observer is not None:
-            self.observer(index, "wo", o)
-        return self._row_linear(o, layer.wo)
+        return o.reshape(*o.shape[:2], -1)
 
     def _linear(self, x: torch.Tensor, weight):
         """A projection whose consumer is one of the engine's fused elementwise kernels: without tensor

@@ -6,10 +6,12 @@ and the matching columns of ``w_down``, and vocabulary rows ``[r*V/P, (r+1)*V/P)
 embedding and drafters are replicated. Every rank therefore holds identical residual streams after each
 all-reduce, computes identical draft trees and acceptance decisions, and no control data is broadcast.
 
-The two row-parallel projections of a block end in an all-reduce of ``[tokens, hidden]``. :class:`TPGroup` runs it
-through NCCL (the baseline) or, with ``fused=True``, through :mod:`economize_b200.parallel.comm`: the row-parallel
-GEMM pushes its partial tiles straight into every peer's IPC-mapped receive buffer over NVLink and the following
-RMSNorm sums the ranks' partials (in rank order, so every rank gets bit-identical results).
+The two row-parallel projections of a block end in a reduction of ``[tokens, hidden]`` over the ranks. With NCCL
+(the baseline) it is an all-reduce of the full rows. With ``fused=True`` a pass runs sequence-parallel through
+:mod:`economize_b200.parallel.sp`: the row-parallel GEMM stores every output row into its owner rank's slot over
+NVLink (GEMM -> reduce-scatter), the owner sums the ranks' partials in rank order, adds the residual, applies the
+next RMSNorm and pushes the normed rows to every rank, and the next column-parallel GEMM waits for them
+(all-gather -> GEMM); every rank gets bit-identical rows.
 Economize relies on ``transformers``' ``tp_plan="auto"`` with DTensor (``src/economize/distributed/tp.py:117-138``).
 """
 
@@ -34,6 +36,8 @@ class TPGroup:
     group: object = None
     fused: bool = False
     comm: object = None
+    #: the sequence-parallel fused collectives (parallel/sp.py); passes they cannot carry take NCCL
+    sp: object = None
 
     def all_reduce(self, x: torch.Tensor) -> torch.Tensor:
         if self.size == 1:

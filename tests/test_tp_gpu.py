@@ -57,6 +57,36 @@ def _worker(rank, world, port, queue):
         dist.all_gather(every, probe)
         result["identical"] = all(torch.equal(every[0], e) for e in every)
         comm.close()
+        # sequence-parallel collectives: GEMM -> reduce-scatter -> reduce + residual + RMSNorm -> all-gather -> GEMM
+        # against an NCCL all-reduce of the same partials
+        from economize_b200.parallel.sp import SequenceParallel
+
+        sp = SequenceParallel(tp, 1024, max_rows=256)
+        gw = torch.Generator(device=dev).manual_seed(1000 + rank)
+        w_row = (torch.randn(1024, 512, device=dev, generator=gw) * 0.05).bfloat16()  # this rank's K slice
+        w_col = (torch.randn(768, 1024, device=dev, generator=torch.Generator(device=dev).manual_seed(7)) *
+                 0.05).bfloat16()
+        wn = (1 + 0.1 * torch.randn(1024, device=dev, generator=torch.Generator(device=dev).manual_seed(8))).bfloat16()
+        for rows in (1, 61, 200, 256):
+            x = torch.randn(rows, 512, device=dev, generator=gw).bfloat16()
+            resid = torch.randn(rows, 1024, device=dev, generator=torch.Generator(device=dev).manual_seed(rows)).bfloat16()
+            part = ops.linear(x, w_row)
+            summed = part.float().clone()
+            dist.all_reduce(summed)
+            want_res = (summed.bfloat16().float() + resid.float()).bfloat16()
+            want_norm = ops.rmsnorm(want_res, wn, 1e-5)[0]
+            want_y = ops.linear(want_norm, w_col)
+            for rep in range(3):  # the round parities alternate on the device
+                sp.rs_linear(x, w_row)
+                lo, n = sp.shard(rows)
+                new_res = sp.reduce_norm(resid[lo:lo + n].contiguous(), wn, 1e-5, rows)
+                y = sp.ag_linear(w_col, rows)
+                torch.cuda.synchronize()
+                ok = (new_res.float() - want_res[lo:lo + n].float()).abs().max().item() <= 0.07 if n else True
+                ok = ok and (y.float() - want_y.float()).abs().max().item() <= 0.05 * want_y.abs().max().item() + 0.05
+                result[f"sp{rows}_{rep}"] = bool(ok)
+        sp.check()
+        sp.close()
         # TP decoding, NCCL and fused: greedy-valid tokens identical on all ranks
         cfg = tiny_llama(hidden_size=1024, num_heads=8, num_kv_heads=4, head_dim=128, intermediate_size=2048,
                          num_layers=3)
@@ -75,8 +105,8 @@ def _worker(rank, world, port, queue):
             agree = sum(int((r.tokens == b.tokens).all()) for r, b in zip(out, base))
             result[f"tp_fused{fused}"] = same_ranks and agree >= 1
             if fused:
-                model.tp.comm.check()
-                model.tp.comm.close()
+                model.tp.sp.check()
+                model.tp.sp.close()
             del em, model, out  # release the captured graphs (they hold NCCL calls) before the group goes away
         result["status"] = ops.require().status(rank) == 0
     except Exception as err:  # report instead of hanging the other rank
