@@ -8,6 +8,8 @@ peaks. Ops:
 * ``gemm``       bf16 ``x[M, K] @ w[N, K]^T`` (tcgen05 swap-AB GEMM vs cuBLAS through torch.matmul); calls on
   rotating weight copies (more than 2x L2 in total) are captured in one CUDA graph, so the per-call time excludes
   launch overhead and reads the weights from HBM
+* ``gemm_sweep`` every GEMM variant of the engine and cuBLAS at the decode shapes of Llama-3.1-8B (``--ms`` token
+  counts); one JSON line per shape
 * ``gemm_wq``    weight-only int2 / int4 / int8 / fp8 / mxfp4 / nvfp4 GEMM (``--fmt``), vs the bf16 kernel on the
   same shape
 * ``attention``  tree-masked decode attention over a bf16 slot cache (``--tree`` new tokens per row)
@@ -74,6 +76,42 @@ def bench_gemm(a) -> None:
     nbytes = 2 * (a.m * a.k + a.n * a.k + a.m * a.n)
     _report("gemm_parts" if a.parts else "gemm", {"M": a.m, "N": a.n, "K": a.k, "copies": n_copies}, ours, nbytes,
             2 * a.m * a.n * a.k, base)
+
+
+def bench_gemm_sweep(a) -> None:
+    """Every GEMM variant (``linear_variant`` modes) and cuBLAS at the decode shapes of Llama-3.1-8B: one JSON line
+    per (M, N, K) with the microseconds of each (CUDA graph over rotating weight copies, weights from HBM)."""
+    from .. import ops
+
+    ext = ops.require()
+    dev = torch.device("cuda")
+    hbm, _ = _peaks()
+    shapes = [(6144, 4096), (4096, 4096), (28672, 4096), (4096, 14336), (128256, 4096)]
+    modes = {"cluster": 1, "splitk_lastcta": 2, "stream_k": 3, "parts_2cta": 4, "splitk_2cta_lastcta": 6}
+    for m in a.ms:
+        for n, k in shapes:
+            x = torch.randn(m, k, device=dev).bfloat16()
+            ws = [(torch.randn(n, k, device=dev) * 0.02).bfloat16() for _ in range(_copies(2 * n * k))]
+            row = {"op": "gemm_sweep", "M": m, "N": n, "K": k}
+            nbytes = 2 * (m * k + n * k + m * n)
+            for name, mode in modes.items():
+                try:
+                    t = time_graph([lambda w=w, mode=mode: ext.linear_variant(x, w, mode, 0) for w in ws], a.iters,
+                                   a.warmup)
+                    row[name] = round(t * 1e3, 2)
+                except RuntimeError as err:
+                    row[name] = f"n/a ({str(err)[:40]})"
+            row["default"] = round(time_graph([lambda w=w: ops.linear(x, w) for w in ws], a.iters, a.warmup) * 1e3, 2)
+            row["parts_default"] = round(time_graph([lambda w=w: ops.linear_parts(x, w) for w in ws], a.iters,
+                                                    a.warmup) * 1e3, 2)
+            row["cublas"] = round(time_graph([lambda w=w: torch.matmul(x, w.t()) for w in ws], a.iters,
+                                             a.warmup) * 1e3, 2)
+            best = min(v for v in row.values() if isinstance(v, float))
+            row["roofline_us"] = round(nbytes / hbm / 1e3, 2)
+            row["best_frac_of_measured_hbm"] = round(nbytes / hbm / 1e3 / best, 3)
+            print(json.dumps(row))
+            sys.stdout.flush()
+            del ws
 
 
 def bench_gemm_wq(a) -> None:
@@ -226,7 +264,8 @@ def bench_glu(a) -> None:
 
 def main(argv: list[str] | None = None) -> None:
     p = argparse.ArgumentParser(description=__doc__.splitlines()[0])
-    p.add_argument("op", choices=["gemm", "gemm_wq", "attention", "layer", "teal", "glu", "topk"])
+    p.add_argument("op", choices=["gemm", "gemm_sweep", "gemm_wq", "attention", "layer", "teal", "glu", "topk"])
+    p.add_argument("--ms", type=int, nargs="+", default=[1, 8, 61, 488], help="gemm_sweep: token counts")
     p.add_argument("--topk", type=int, default=10)
     p.add_argument("--m", type=int, default=61)
     p.add_argument("--n", type=int, default=6144)
@@ -243,7 +282,7 @@ def main(argv: list[str] | None = None) -> None:
     p.add_argument("--warmup", type=int, default=3)
     p.add_argument("--once", action="store_true", help="one untimed call (for profiler captures)")
     a = p.parse_args(argv)
-    {"gemm": bench_gemm, "gemm_wq": bench_gemm_wq, "attention": bench_attention, "layer": bench_layer,
+    {"gemm": bench_gemm, "gemm_sweep": bench_gemm_sweep, "gemm_wq": bench_gemm_wq, "attention": bench_attention, "layer": bench_layer,
      "teal": bench_teal, "glu": bench_glu, "topk": bench_topk}[a.op](a)
 
 

@@ -229,26 +229,48 @@ def build_model(model: nn.Module, configs: Sequence[TechniqueConfig], *, decodin
         return t
 
     # weight transforms (which may change the depth or the projections) are built and attached first, so the other
-    # techniques are built against the transformed model
+    # techniques are built against the transformed model. A failure anywhere rolls the whole call back.
+    from .transaction import AttachTransaction
+
     order = sorted(configs, key=lambda c: _rank(technique_for(c)))
     techniques: list[Technique] = []
-    for config in order:
-        if Capability.WEIGHTS in technique_for(config).capabilities:
-            t = build(config)
-            techniques.append(t)
-            check_compatible(techniques)
+    tx = AttachTransaction(engine_model)
+    current = None
+    try:
+        for config in order:
+            if Capability.WEIGHTS in technique_for(config).capabilities:
+                current = None
+                t = build(config)
+                current = t
+                techniques.append(t)
+                check_compatible(techniques)
+                tx.before_weights(t)
+                t.attach()
+                tx.attached_ok(t)
+        current = None
+        rest = [build(c) for c in order if Capability.WEIGHTS not in technique_for(c).capabilities]
+        check_compatible(techniques + rest)
+        for t in rest:
+            current = t
             t.attach()
-    rest = [build(c) for c in order if Capability.WEIGHTS not in technique_for(c).capabilities]
-    check_compatible(techniques + rest)
-    for t in rest:
-        t.attach()
-    techniques += rest
-    for t in techniques:  # drafter transforms (draft_quant, frspec) act once the drafter is attached
-        if hasattr(t, "after_drafter"):
-            drafter = next((d for d in techniques if Capability.DRAFTER in d.capabilities), None)
-            if drafter is None:
-                raise ConfigError(f"{t.name} transforms a drafter, but no drafting technique is applied")
-            t.after_drafter(drafter)
+            tx.attached_ok(t)
+        current = None
+        techniques += rest
+        for t in techniques:  # drafter transforms (draft_quant, frspec) act once the drafter is attached
+            if hasattr(t, "after_drafter"):
+                drafter = next((d for d in techniques if Capability.DRAFTER in d.capabilities), None)
+                if drafter is None:
+                    raise ConfigError(f"{t.name} transforms a drafter, but no drafting technique is applied")
+                current = t
+                t.after_drafter(drafter)
+    except BaseException as error:
+        if current is not None and Capability.WEIGHTS not in current.capabilities:
+            try:  # a technique that raised part way through its own attach is detached too
+                current.detach()
+            except Exception:  # noqa: BLE001 - the original error is the one to report
+                pass
+        tx.roll_back(current, error)
+        raise
     if decoding is None:
         decoding = next((d for t in techniques if (d := t.default_decoding()) is not None), None)
     if decoding is None:

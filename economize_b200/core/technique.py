@@ -117,6 +117,11 @@ class Technique(nn.Module):
     def detach(self) -> None:
         """Undo :meth:`attach` where possible."""
 
+    def inplace_targets(self) -> list[torch.Tensor]:
+        """Tensors of the model that :meth:`attach` changes in place (rather than replacing them), so that a failed
+        ``apply`` can restore their contents. Weight techniques that write into existing tensors list them."""
+        return []
+
     def drafter(self) -> DraftModel | None:
         return None
 

@@ -41,7 +41,8 @@ class DecodeConfig:
             ``cuda_graphs`` is on.
         draft_policy_options: Options of the draft policy (``{"depth": 6, "topk": 10, "total_tokens": 60}``).
         prefill_chunk: Prefill prompts in chunks of this many tokens.
-        window_cache: Ring caches for sliding-window layers (accepted for compatibility).
+        window_cache: Ring caches for sliding-window layers. This engine keeps one contiguous slot cache for every
+            layer, so ``True`` is refused with :class:`~economize_b200.errors.ConfigError` rather than ignored.
     """
 
     cycle_length: int = 4
@@ -64,8 +65,9 @@ class DecodeConfig:
         check_positive("sync_interval", self.sync_interval)
         if self.prefill_chunk is not None:
             check_positive("prefill_chunk", self.prefill_chunk)
-        if self.window_cache and self.prefill_chunk is None:
-            raise ConfigError("window_cache needs prefill_chunk")
+        if self.window_cache:
+            raise ConfigError("window_cache=True asks for ring caches of sliding-window layers, which this engine "
+                              "does not build (every layer keeps a contiguous slot cache); leave it False")
         if self.min_confidence is not None:
             check_unit_interval("min_confidence", self.min_confidence, closed_high=True)
         for name in ("verifier_options", "draft_policy_options"):

@@ -92,6 +92,16 @@ class PruneTechnique(Technique):
             i, name = key.split(":")
             install(model.layers[int(i)], name, sw.to(model.device))
 
+    def inplace_targets(self) -> list[torch.Tensor]:
+        """Unstructured and N:M pruning write the masked weights into the existing projections."""
+        if not hasattr(self, "_targets"):
+            return []
+        out = []
+        for i, names in self._targets().items():
+            layer = self.model.layers[i]
+            out += [getattr(layer, n) for n in names if isinstance(getattr(layer, n), torch.Tensor)]
+        return out
+
     def technique_state(self) -> dict[str, torch.Tensor]:
         out = {}
         for key, sw in self.weights.items():

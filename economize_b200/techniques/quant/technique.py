@@ -202,6 +202,18 @@ class QuantTechnique(_QuantBase):
                     self.replaced[f"{i}:wqkv"] = layer.wqkv.detach().clone()
                 self._awq_scale[(i, name)] = (1.0 / s)[None, :]
 
+    def inplace_targets(self) -> list[torch.Tensor]:
+        """AWQ and SmoothQuant fold their scales into the projections and norms of the quantized layers in place."""
+        if self.weights or self.config.method not in ("awq", "smoothquant"):
+            return []
+        layers = [i - 1 for i in self.config.layers] if self.config.layers else range(self.model.config.num_layers)
+        out = []
+        for i in layers:
+            layer = self.model.layers[i]
+            out += [t for t in (layer.attn_norm, layer.mlp_norm, layer.wqkv, layer.wo, layer.w_gate_up, layer.w_down)
+                    if isinstance(t, torch.Tensor)]
+        return out
+
     def attach(self) -> None:
         if not self.weights:
             self._quantize()
