@@ -421,11 +421,11 @@ def run_reference_tp(ref, args, world, rank, log):
     else:
         return None, "reference tensor-parallel decoding failed: " + " | ".join(errors)
     path = _cache_path(args, "reference", 0)
-    if os.path.exists(path):
+    if os.path.exists(path):  # the drafter the 1-GPU reference run trained on this box
         arm.load_state(torch.load(path, map_location="cuda", weights_only=True))
     else:
-        try:
-            train_drafter(arm, args, prompts, path + f".tp{world}.r{rank}", log)
+        try:  # every rank runs the same recipe (the reference's fit joins its own collectives on all of them)
+            train_drafter(arm, args, prompts, path + f".tp{world}", log)
         except Exception as err:
             return None, f"reference drafter training on a tensor-parallel model failed: {err}"
     rows = list(prompts)
@@ -503,12 +503,10 @@ def run_ours(args, world, rank, log):
 
         from economize_b200.distributed import TPGroup, tensor_parallel
 
-        path = _cache_path(args, "ours", 0)
-        if rank == 0:
-            train_drafter(arm, args, prompts, path, log)
+        # every rank runs the same recipe on the same stream (train.fit averages the identical gradients over the
+        # ranks, so no rank waits in a collective the others do not join), then rank 0's weights are broadcast
+        train_drafter(arm, args, prompts, _cache_path(args, "ours", 0) + f".tp{world}", log)
         dist.barrier()
-        if rank != 0:
-            train_drafter(arm, args, prompts, path, log)  # loads rank 0's weights
         for tensor in arm.tech.state_dict().values():  # bit-identical drafters: every rank drafts the same tree
             dist.broadcast(tensor, src=0)
         tensor_parallel(arm.model, TPGroup(rank, world), fused=not args.nccl_tp)

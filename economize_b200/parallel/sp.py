@@ -94,9 +94,14 @@ class SequenceParallel:
             raise CommTimeoutError(f"a peer's rows did not arrive in time (status {status})")
 
     def close(self) -> None:
+        """Unmap the peers' buffers and free this rank's. Every rank calls it (it waits for the others first, so no
+        peer still stores into a buffer being freed)."""
+        if not self.ptrs:
+            return
+        torch.cuda.synchronize()
+        dist.barrier(group=self.tp.group)
         for r, p in enumerate(self.ptrs):
             if r != self.tp.rank:
                 self.ext.symm_close(p)
-        if self.ptrs:
-            self.ext.symm_free(self.own)
+        self.ext.symm_free(self.own)
         self.ptrs = []
