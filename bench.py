@@ -333,7 +333,8 @@ class RefArm:
         return {k: tuple(v.shape) for k, v in self.tech.state_dict().items()}
 
     def lm_head(self):
-        return self.hf.lm_head.weight
+        w = self.hf.lm_head.weight
+        return w.full_tensor() if hasattr(w, "full_tensor") else w  # a tp_plan-sharded head is gathered
 
     def state(self):
         return self.tech.state_dict()
@@ -420,14 +421,10 @@ def run_reference_tp(ref, args, world, rank, log):
         break
     else:
         return None, "reference tensor-parallel decoding failed: " + " | ".join(errors)
-    path = _cache_path(args, "reference", 0)
-    if os.path.exists(path):  # the drafter the 1-GPU reference run trained on this box
-        arm.load_state(torch.load(path, map_location="cuda", weights_only=True))
-    else:
-        try:  # every rank runs the same recipe (the reference's fit joins its own collectives on all of them)
-            train_drafter(arm, args, prompts, path + f".tp{world}", log)
-        except Exception as err:
-            return None, f"reference drafter training on a tensor-parallel model failed: {err}"
+    try:  # the recipe on the sharded model, on every rank (the reference's fit joins its collectives on all)
+        train_drafter(arm, args, prompts, _cache_path(args, "reference", 0) + f".tp{world}", log)
+    except Exception as err:
+        return None, f"reference drafter training on a tensor-parallel model failed: {type(err).__name__}: {err}"
     rows = list(prompts)
     results = {"cfg": arm.spec_cfg, "attn": arm.attn, "streams": 1}
 
@@ -446,6 +443,7 @@ class OursArm:
 
         self.eco, self.args = eco, args
         self.target = target
+        self.full_head = target.head_weight.detach()  # kept whole: sharding replaces the parameter's data
         self.vocab = target.config.vocab_size
         self.model = eco.apply(target, Eagle3Config(draft_vocab=min(DRAFT_VOCAB, self.vocab)))
         self.tech = self.model.techniques["eagle3"]
@@ -463,7 +461,7 @@ class OursArm:
         return {k: tuple(v.shape) for k, v in to_reference_state(self.tech).items()}
 
     def lm_head(self):
-        return self.target.head_weight
+        return self.full_head
 
     def state(self):
         from economize_b200.techniques.eagle3.formats import to_reference_state
@@ -503,13 +501,16 @@ def run_ours(args, world, rank, log):
 
         from economize_b200.distributed import TPGroup, tensor_parallel
 
-        # every rank runs the same recipe on the same stream (train.fit averages the identical gradients over the
-        # ranks, so no rank waits in a collective the others do not join), then rank 0's weights are broadcast
-        train_drafter(arm, args, prompts, _cache_path(args, "ours", 0) + f".tp{world}", log)
+        # the recipe runs on the sharded model: a sharded target sums its partials in another order than one GPU,
+        # so its greedy trajectory (what the drafter learns) is its own. Every rank runs the same steps on the same
+        # stream (train.fit averages the identical gradients over the ranks, so no rank waits alone in a
+        # collective), then rank 0's weights are broadcast
+        tensor_parallel(arm.model, TPGroup(rank, world), fused=not args.nccl_tp)
+        train_drafter(arm, args, prompts, _cache_path(args, "ours", 0) + f".tp{world}" +
+                      ("-nccl" if args.nccl_tp else ""), log)
         dist.barrier()
         for tensor in arm.tech.state_dict().values():  # bit-identical drafters: every rank drafts the same tree
             dist.broadcast(tensor, src=0)
-        tensor_parallel(arm.model, TPGroup(rank, world), fused=not args.nccl_tp)
     else:
         train_drafter(arm, args, prompts, _cache_path(args, "ours", stream), log)
     rows = list(prompts)
