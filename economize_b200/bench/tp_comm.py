@@ -48,6 +48,8 @@ def main(argv: list[str] | None = None) -> None:
     p.add_argument("--n", type=int, default=6144, help="full output width of the column-parallel projection")
     p.add_argument("--iters", type=int, default=200)
     p.add_argument("--warmup", type=int, default=20)
+    p.add_argument("--breakdown", action="store_true", help="also print each kernel's device time per boundary "
+                   "(CUPTI records of eager calls, rank 0)")
     a = p.parse_args(argv)
     tp = init_distributed("nccl", timeout_s=60)
     rank, world = tp.rank, tp.size
@@ -104,6 +106,24 @@ def main(argv: list[str] | None = None) -> None:
         out[name] = max_over_ranks(s.elapsed_time(e) / a.iters, dev) * 1e3  # us
         del graph  # released before the process group is destroyed
         dist.barrier(group=tp.group)
+    if a.breakdown:
+        from torch.profiler import ProfilerActivity, profile
+
+        for name, fn in (("sp", fused_sp), ("nccl", nccl)):
+            torch.cuda.synchronize()
+            dist.barrier(group=tp.group)
+            with profile(activities=[ProfilerActivity.CUDA]) as prof:
+                for _ in range(20):
+                    fn()
+                torch.cuda.synchronize()
+            dist.barrier(group=tp.group)
+            per: dict[str, float] = {}
+            for ev in prof.events():
+                if ev.device_type == torch.autograd.DeviceType.CUDA:
+                    per[ev.name[:60]] = per.get(ev.name[:60], 0.0) + ev.device_time_total / 20
+            if rank == 0:
+                print(json.dumps({"breakdown": name, "us_per_boundary": {k: round(v, 2) for k, v in
+                                                                         sorted(per.items(), key=lambda kv: -kv[1])}}))
     sp.check()
     comm.check()
     hw = HARDWARE["b200"]  # the measured copy bandwidth and cuBLAS bf16 peak of this pool

@@ -262,7 +262,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   // exact-tail mode: this row's tensor-core keys are the committed slots below its position minus tail_w
   int tc_lim = 0;
   if (tail && row_valid) {
-    const int depth = use_mask ? (__popcll(bits) - 1) : (q_offset + t);
+    const int depth = max(0, use_mask ? (__popcll(bits) - 1) : (q_offset + t));
     tc_lim = max(0, min(base, base + depth - tail_w));
   }
   int visible_end = tail ? base : use_mask ? base + nn : base + min(nn, q_offset + t_last + 1);
@@ -553,6 +553,9 @@ __device__ __forceinline__ float tail_score(const float4& qv, const float4& kv, 
   return warp_sum(d) * scale_log2;
 }
 
+constexpr int kTailKeysMax = 128;  // committed tail (tail_w <= 64) + new keys (at most 64)
+constexpr int kTailBatch = 8;      // keys whose loads are issued together
+
 __global__ void __launch_bounds__(128) attn_merge_tail_kernel(
     const float* __restrict__ ws_o, const float* __restrict__ ws_ml, bf16* __restrict__ out, int T, int H, int Hkv,
     int m_tiles, int splits, float* __restrict__ lse_out, const bf16* __restrict__ q,
@@ -560,9 +563,12 @@ __global__ void __launch_bounds__(128) attn_merge_tail_kernel(
     const int* __restrict__ n_new, const int64_t* __restrict__ mask, int S, float scale_log2, int q_offset,
     int tail_w, const float* __restrict__ k_scale, const float* __restrict__ v_scale,
     const uint32_t* __restrict__ keep) {
+  __shared__ int s_row[4][kTailKeysMax];    // cache rows of this warp's tail keys, in position order
+  __shared__ float s_sc[4][kTailKeysMax];   // their scaled scores
   pdl_trigger();
   pdl_wait();
-  const int tile = blockIdx.x, r = blockIdx.y * 4 + (threadIdx.x >> 5), lane = threadIdx.x & 31;
+  const int wid = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int tile = blockIdx.x, r = blockIdx.y * 4 + wid;
   const int m_tile = tile % m_tiles, bh = tile / m_tiles;
   const int b = bh / Hkv, kvh = bh % Hkv;
   const int G = H / Hkv;
@@ -576,28 +582,57 @@ __global__ void __launch_bounds__(128) attn_merge_tail_kernel(
   const int base = kv_len[b], nn = n_new[b];
   const bool use_mask = mask != nullptr;
   const uint64_t bits = use_mask ? static_cast<uint64_t>(mask[static_cast<size_t>(b) * T + t]) : 0ull;
-  const int depth = use_mask ? (__popcll(bits) - 1) : (q_offset + t);
+  const int depth = max(0, use_mask ? (__popcll(bits) - 1) : (q_offset + t));  // a row seeing no new key: 0
   const int lo = max(0, base + depth - tail_w);
   const size_t row0 = (static_cast<size_t>(b) * Hkv + kvh) * S;
   const float4 qv = load_kv4(reinterpret_cast<const uint8_t*>(q),
                              (static_cast<size_t>(b) * T + t) * H + head, lane, false);
-  auto committed_visible = [&](int s) -> bool {
-    return keep == nullptr || ((keep[(static_cast<size_t>(b) * Hkv + kvh) * (S / 32) + s / 32] >> (s & 31)) & 1u);
-  };
-  auto new_visible = [&](int j) -> bool { return use_mask ? ((bits >> j) & 1ull) != 0ull : j <= q_offset + t; };
   const int n_end = min(nn, use_mask ? 64 : q_offset + t + 1);
 
-  // the maximum over the splits' partials and the tail's scores
+  // the tail keys in position order: committed slots [lo, base) the keep bitmap shows, then the row's own new keys
+  // (ancestors and itself, in depth order), compacted with warp ballots
+  int n_keys = 0;
+  for (int s0 = lo; s0 < base; s0 += 32) {
+    const int s = s0 + lane;
+    bool vis = s < base;
+    if (vis && keep != nullptr)
+      vis = (keep[(static_cast<size_t>(b) * Hkv + kvh) * (S / 32) + s / 32] >> (s & 31)) & 1u;
+    const unsigned ballot = __ballot_sync(0xffffffffu, vis);
+    if (vis) s_row[wid][n_keys + __popc(ballot & ((1u << lane) - 1u))] = static_cast<int>(s);
+    n_keys += __popc(ballot);
+  }
+  for (int j0 = 0; j0 < n_end; j0 += 32) {
+    const int j = j0 + lane;
+    const bool vis = j < n_end && (use_mask ? ((bits >> j) & 1ull) != 0ull : j <= q_offset + t);
+    const unsigned ballot = __ballot_sync(0xffffffffu, vis);
+    if (vis) s_row[wid][n_keys + __popc(ballot & ((1u << lane) - 1u))] = base + j;
+    n_keys += __popc(ballot);
+  }
+  __syncwarp();
+
+  // scores, batches of kTailBatch keys whose K loads are in flight together
   float mx = -INFINITY;
   for (int sp = 0; sp < splits; ++sp) {
     const size_t slot = (static_cast<size_t>(tile) * splits + sp) * kRows + r;
     if (ws_ml[slot * 2 + 1] > 0.f) mx = fmaxf(mx, ws_ml[slot * 2]);
   }
-  for (int s = lo; s < base; ++s)
-    if (committed_visible(s)) mx = fmaxf(mx, tail_score(qv, load_kv4(k_cache, row0 + s, lane, fp8), sl));
-  for (int j = 0; j < n_end; ++j)
-    if (new_visible(j)) mx = fmaxf(mx, tail_score(qv, load_kv4(k_cache, row0 + base + j, lane, fp8), sl));
+  for (int i0 = 0; i0 < n_keys; i0 += kTailBatch) {
+    float4 kv[kTailBatch];
+#pragma unroll
+    for (int u = 0; u < kTailBatch; ++u)
+      if (i0 + u < n_keys) kv[u] = load_kv4(k_cache, row0 + s_row[wid][i0 + u], lane, fp8);
+#pragma unroll
+    for (int u = 0; u < kTailBatch; ++u) {
+      if (i0 + u < n_keys) {
+        const float sc = tail_score(qv, kv[u], sl);
+        if (lane == 0) s_sc[wid][i0 + u] = sc;
+        mx = fmaxf(mx, sc);
+      }
+    }
+  }
+  __syncwarp();
 
+  // the splits' partials, then the tail keys in position order
   float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
   float denom = 0.f;
   for (int sp = 0; sp < splits; ++sp) {
@@ -609,17 +644,22 @@ __global__ void __launch_bounds__(128) attn_merge_tail_kernel(
     acc.x += v.x * w; acc.y += v.y * w; acc.z += v.z * w; acc.w += v.w * w;
     denom += l * w;
   }
-  auto add_key = [&](size_t row) {
-    const float w = exp2f(tail_score(qv, load_kv4(k_cache, row, lane, fp8), sl) - mx);
-    float4 v = load_kv4(v_cache, row, lane, fp8);
-    v.x *= sv; v.y *= sv; v.z *= sv; v.w *= sv;
-    acc.x += v.x * w; acc.y += v.y * w; acc.z += v.z * w; acc.w += v.w * w;
-    denom += w;
-  };
-  for (int s = lo; s < base; ++s)
-    if (committed_visible(s)) add_key(row0 + s);
-  for (int j = 0; j < n_end; ++j)
-    if (new_visible(j)) add_key(row0 + base + j);
+  for (int i0 = 0; i0 < n_keys; i0 += kTailBatch) {
+    float4 vv[kTailBatch];
+#pragma unroll
+    for (int u = 0; u < kTailBatch; ++u)
+      if (i0 + u < n_keys) vv[u] = load_kv4(v_cache, row0 + s_row[wid][i0 + u], lane, fp8);
+#pragma unroll
+    for (int u = 0; u < kTailBatch; ++u) {
+      if (i0 + u < n_keys) {
+        const float w = exp2f(s_sc[wid][i0 + u] - mx);
+        float4 v = vv[u];
+        v.x *= sv; v.y *= sv; v.z *= sv; v.w *= sv;
+        acc.x += v.x * w; acc.y += v.y * w; acc.z += v.z * w; acc.w += v.w * w;
+        denom += w;
+      }
+    }
+  }
 
   const float inv = denom > 0.f ? 1.f / denom : 0.f;
   if (lse_out != nullptr && lane == 0)

@@ -31,7 +31,7 @@ namespace ecz {
 
 namespace {
 
-constexpr int kRowsPerCta = 4;
+constexpr int kRowsPerCta = 1;  // one row per CTA: a boundary of M rows runs M / P CTAs in parallel
 
 __device__ __forceinline__ unsigned ld_acquire_sys32(const unsigned* p) {
   unsigned v;
