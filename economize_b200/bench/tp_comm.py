@@ -82,8 +82,20 @@ def main(argv: list[str] | None = None) -> None:
         h, _ = comm.reduce_rmsnorm(comm.gemm_push(x, w_row), norm, 1e-5, resid)
         return ops.linear(h, w_col)
 
+    h_full = torch.randn(a.rows, a.hidden, device=dev, generator=g).bfloat16()
+
+    def sp_no_col():  # the collective half alone: the all-gather round consumed by a copy instead of the GEMM
+        sp.rs_linear(x, w_row)
+        sp.reduce_norm(resid_own, norm, 1e-5, a.rows)
+        return sp.fetch(a.rows, x)
+
+    def gemms():  # the two projections alone, on local tensors
+        ops.linear(x, w_row)
+        return ops.linear(h_full, w_col)
+
     out = {}
-    for name, fn in (("sp", fused_sp), ("nccl", nccl), ("fused_ar", fused_ar)):
+    for name, fn in (("sp", fused_sp), ("nccl", nccl), ("fused_ar", fused_ar), ("sp_no_col_gemm", sp_no_col),
+                     ("gemms_only", gemms)):
         for _ in range(a.warmup):
             fn()
         torch.cuda.synchronize()
@@ -137,6 +149,8 @@ def main(argv: list[str] | None = None) -> None:
         print(json.dumps({"op": "row_gemm_rs_norm_ag_col_gemm", "ranks": world, "M": a.rows, "H": a.hidden,
                           "K": a.k, "N": a.n, "sp_us": round(out["sp"], 2), "nccl_us": round(out["nccl"], 2),
                           "fused_allreduce_us": round(out["fused_ar"], 2),
+                          "sp_without_column_gemm_us": round(out["sp_no_col_gemm"], 2),
+                          "two_gemms_alone_us": round(out["gemms_only"], 2),
                           "sp_vs_nccl": round(out["nccl"] / out["sp"], 3), "roofline_us": round(roof, 2),
                           "roofline_terms_us": {"hbm": round(t_hbm, 2), "tensor": round(t_flop, 3),
                                                 "nvlink": round(t_link, 2)},

@@ -803,11 +803,26 @@ int gemm_splits(int M, int N, int K, int num_sms) {
   return std::max(1, std::min(splits, 16));
 }
 
+template <int BN>
+int cluster_capacity_bn(int splits);
+
 // Split count of the cluster split-K kernel: the gemm_splits rule over the CTA slots (two per SM for skinny
-// tiles), capped at 8 CTAs per (portable) cluster. Identical for every M up to 64 rows.
+// tiles), capped at 8 CTAs per (portable) cluster, then lowered until every tile's cluster is resident at once
+// (the hardware places clusters inside GPCs, so a tile grid larger than the resident clusters runs in waves).
+// Identical for every M up to 64 rows (the 64-row configuration's capacity stands for both skinny tile widths), so
+// one-token and verification passes reduce K the same way.
 int gemm_cluster_splits(int M, int N, int K, int num_sms) {
-  const int slots = gemm_block_n(M) <= 64 ? 2 * num_sms : num_sms;
-  return std::min(8, gemm_splits(M, N, K, slots));
+  const int bn = gemm_block_n(M);
+  const int slots = bn <= 64 ? 2 * num_sms : num_sms;
+  int splits = std::min(8, gemm_splits(M, N, K, slots));
+  const int tiles = ((N + kBM - 1) / kBM) * ((M + bn - 1) / bn);
+  while (splits > 1) {
+    const int cap = bn <= 64 ? cluster_capacity_bn<64>(splits)
+                  : bn == 128 ? cluster_capacity_bn<128>(splits) : cluster_capacity_bn<256>(splits);
+    if (tiles <= cap) break;
+    --splits;
+  }
+  return splits;
 }
 
 // How many clusters of `splits` CTAs of the BN-wide cluster kernel can be resident at once (the hardware packs
