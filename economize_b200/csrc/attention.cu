@@ -47,6 +47,9 @@ constexpr int kDim = 128;
 constexpr int kAtom = kRows * 128;          // bytes of one 64-column swizzled half tile (128 rows x 128 B)
 constexpr int kTile = 2 * kAtom;            // a 128 x 128 bf16 tile
 constexpr int kSmem = 6 * kTile + 1024 + 64 + 4 * 128 * 4;  // Q, P, 2 x K, 2 x V, barriers, row partials
+// the same layout for head dimension D (Q [128, D], P [128, 128], two stages of K and V [128, D])
+__host__ __device__ constexpr int attn_smem_bytes(int D) { return kRows * D * 2 + kTile + 4 * kKeys * D * 2 + 1024 + 64 + 4 * 128 * 4; }
+static_assert(attn_smem_bytes(128) == kSmem, "the D = 128 layout is the reference footprint");
 constexpr int kRawTile = kKeys * kDim;                        // one fp8 code tile (128 keys x 128 B)
 // fp8: Q, P, converted K, converted V, then 2 stages x (raw K, raw V): the same 6 x kTile
 static_assert(4 * kTile + 4 * kRawTile == 6 * kTile, "fp8 layout must fit the bf16 footprint");
@@ -168,7 +171,8 @@ __device__ __forceinline__ float fast_exp2(float x) {
 }
 
 // Combine the split partials of packed row r of tile `tile`: out = sum_s O_s 2^(m_s - M) / sum_s l_s 2^(m_s - M).
-// One warp per row, lane l owns columns 4l .. 4l + 3.
+// One warp per row, lane l owns columns E l .. E l + E - 1 (E = D / 32).
+template <int D>
 __device__ __forceinline__ void merge_row(const float* __restrict__ ws_o, const float* __restrict__ ws_ml,
                                           bf16* __restrict__ out, int tile, int r, int lane, int T, int H, int Hkv,
                                           int m_tiles, int splits, float* __restrict__ lse_out) {
@@ -184,30 +188,35 @@ __device__ __forceinline__ void merge_row(const float* __restrict__ ws_o, const 
     const size_t slot = (static_cast<size_t>(tile) * splits + s) * kRows + r;
     if (ws_ml[slot * 2 + 1] > 0.f) mx = fmaxf(mx, ws_ml[slot * 2]);
   }
-  float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+  constexpr int E = D / 32;
+  float acc[E];
+#pragma unroll
+  for (int e = 0; e < E; ++e) acc[e] = 0.f;
   float denom = 0.f;
   for (int s = 0; s < splits; ++s) {
     const size_t slot = (static_cast<size_t>(tile) * splits + s) * kRows + r;
     const float l = ws_ml[slot * 2 + 1];
     if (!(l > 0.f)) continue;
     const float w = exp2f(ws_ml[slot * 2] - mx);
-    const float4 v = reinterpret_cast<const float4*>(ws_o + slot * kDim)[lane];
-    acc.x += v.x * w; acc.y += v.y * w; acc.z += v.z * w; acc.w += v.w * w;
+    const float* v = ws_o + slot * D + lane * E;
+#pragma unroll
+    for (int e = 0; e < E; ++e) acc[e] += v[e] * w;
     denom += l * w;
   }
   const float inv = denom > 0.f ? 1.f / denom : 0.f;
   if (lse_out != nullptr && lane == 0)
     lse_out[(static_cast<size_t>(b) * T + t) * H + head] = denom > 0.f ? mx + __log2f(denom) : -INFINITY;
-  bf16* dst = out + ((static_cast<size_t>(b) * T + t) * H + head) * kDim + lane * 4;
-  *reinterpret_cast<__nv_bfloat162*>(dst) = __floats2bfloat162_rn(acc.x * inv, acc.y * inv);
-  *reinterpret_cast<__nv_bfloat162*>(dst + 2) = __floats2bfloat162_rn(acc.z * inv, acc.w * inv);
+  bf16* dst = out + ((static_cast<size_t>(b) * T + t) * H + head) * D + lane * E;
+#pragma unroll
+  for (int e = 0; e < E; e += 2)
+    *reinterpret_cast<__nv_bfloat162*>(dst + e) = __floats2bfloat162_rn(acc[e] * inv, acc[e + 1] * inv);
 }
 
 // 16 warps: warp w reads TMEM lanes 32 * (w % 4) .. (its rows) and owns score / output columns
 // [32 * (w / 4), 32 * (w / 4) + 32) of them (quarter q).
 constexpr int kThreads = 512;
 
-template <bool FP8>
+template <bool FP8, int D = 128>
 __global__ void __launch_bounds__(kThreads, 1)
     attn_tc_kernel(const bf16* __restrict__ q, const __grid_constant__ CUtensorMap tm_k,
                    const __grid_constant__ CUtensorMap tm_v, bf16* __restrict__ out, float* __restrict__ ws_o,
@@ -219,18 +228,24 @@ __global__ void __launch_bounds__(kThreads, 1)
                    const uint8_t* __restrict__ kivi, const int* __restrict__ kivi_chunks, int kivi_bits, int tail_w) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  static_assert(D == 64 || D == 128, "head dimensions 64 and 128");
+  static_assert(!FP8 || D == 128, "fp8 caches at head dimension 128");
+  constexpr int kQTile = kRows * D * 2;    // Q [128 rows, D]
+  constexpr int kKVTile = kKeys * D * 2;   // one K or V chunk [128 keys, D]
+  constexpr int kDQ = D / 4;               // output columns per quarter of the CTA
+  constexpr int kAtoms = D / 64;           // 64-column swizzled atoms per row
   uint8_t* q_tile = smem;
-  uint8_t* p_tile = smem + kTile;
+  uint8_t* p_tile = smem + kQTile;
   // bf16: two stages of K and V tiles; fp8: one converted K and V tile, then two stages of raw codes
-  uint8_t* k_tiles = smem + 2 * kTile;
-  uint8_t* v_tiles = FP8 ? smem + 3 * kTile : smem + 4 * kTile;
+  uint8_t* k_tiles = p_tile + kTile;
+  uint8_t* v_tiles = FP8 ? k_tiles + kTile : k_tiles + 2 * kKVTile;
   uint8_t* raw = smem + 4 * kTile;  // fp8 stage s: raw K at s * 2 * kRawTile, raw V after it
-  uint64_t* kv_full = reinterpret_cast<uint64_t*>(smem + 6 * kTile);
+  uint64_t* kv_full = reinterpret_cast<uint64_t*>(p_tile + kTile + 4 * kKVTile);
   uint64_t* bar_s = kv_full + 2;
   uint64_t* bar_pv = bar_s + 1;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bar_pv + 1);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
-  float* red = reinterpret_cast<float*>(smem + 6 * kTile + 64);  // [4][128] row partials
+  float* red = reinterpret_cast<float*>(reinterpret_cast<uint8_t*>(kv_full) + 64);  // [4][128] row partials
 
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int quad = warp & 3, quarter = warp >> 2;
@@ -284,11 +299,12 @@ __global__ void __launch_bounds__(kThreads, 1)
       tma_load_2d(raw + s * 2 * kRawTile, &tm_k, &kv_full[s], 0, y);
       tma_load_2d(raw + s * 2 * kRawTile + kRawTile, &tm_v, &kv_full[s], 0, y);
     } else {
-      mbar_arrive_expect_tx(&kv_full[s], 4 * kAtom);
-      tma_load_2d(k_tiles + s * kTile, &tm_k, &kv_full[s], 0, y);
-      tma_load_2d(k_tiles + s * kTile + kAtom, &tm_k, &kv_full[s], 64, y);
-      tma_load_2d(v_tiles + s * kTile, &tm_v, &kv_full[s], 0, y);
-      tma_load_2d(v_tiles + s * kTile + kAtom, &tm_v, &kv_full[s], 64, y);
+      mbar_arrive_expect_tx(&kv_full[s], 2 * kAtoms * kAtom);
+#pragma unroll
+      for (int a = 0; a < kAtoms; ++a) {
+        tma_load_2d(k_tiles + s * kKVTile + a * kAtom, &tm_k, &kv_full[s], 64 * a, y);
+        tma_load_2d(v_tiles + s * kKVTile + a * kAtom, &tm_v, &kv_full[s], 64 * a, y);
+      }
     }
   };
   // Chunks whose committed keys are all hidden by the keep bitmap (and that hold no new key) are skipped: the
@@ -319,13 +335,13 @@ __global__ void __launch_bounds__(kThreads, 1)
   __syncwarp();
   if (warp == 0) tmem_alloc(tmem_slot, 256);
 
-  // Q row r, chunks [4 * quarter, 4 * quarter + 4) -> swizzled K-major tile (zeros for padding rows)
+  // Q row r, 16-byte chunks [quarter * D / 32, + D / 32) -> swizzled K-major tile (zeros for padding rows)
   {
-    const uint4* src = reinterpret_cast<const uint4*>(q + (static_cast<size_t>(b) * T + t) * H * kDim +
-                                                      static_cast<size_t>(head) * kDim);
+    const uint4* src = reinterpret_cast<const uint4*>(q + (static_cast<size_t>(b) * T + t) * H * D +
+                                                      static_cast<size_t>(head) * D);
 #pragma unroll
-    for (int c = 0; c < 4; ++c) {
-      const int chunk = quarter * 4 + c;
+    for (int c = 0; c < D / 32; ++c) {
+      const int chunk = quarter * (D / 32) + c;
       store_row_swizzled(q_tile, r, chunk, row_valid ? src[chunk] : make_uint4(0, 0, 0, 0));
     }
   }
@@ -336,15 +352,16 @@ __global__ void __launch_bounds__(kThreads, 1)
   const uint32_t tmem = *tmem_slot;
   if (stamp) stamp[1] = global_timer_ns();
   const uint32_t lane_off = static_cast<uint32_t>(quad * 32) << 16;
-  const uint32_t col0 = quarter * 32;
-  const uint32_t tmem_s = tmem + col0, tmem_pv = tmem + 128 + col0;
+  const uint32_t col0 = quarter * 32;        // this quarter's score columns
+  const uint32_t ocol0 = quarter * kDQ;      // this quarter's output columns
+  const uint32_t tmem_s = tmem + col0, tmem_pv = tmem + 128 + ocol0;
 
-  float o[32];
+  float o[kDQ];
 #pragma unroll
-  for (int d = 0; d < 32; ++d) o[d] = 0.f;
+  for (int d = 0; d < kDQ; ++d) o[d] = 0.f;
   float m_run = -INFINITY, l_run = 0.f;
   constexpr uint32_t idesc_s = idesc_bf16_f32(kRows, kKeys);
-  constexpr uint32_t idesc_pv = idesc_bf16_f32(kRows, kDim, /*b_mn_major=*/true);
+  constexpr uint32_t idesc_pv = idesc_bf16_f32(kRows, D, /*b_mn_major=*/true);
   bool ok = true;
 
   int c = next_active(c0);
@@ -365,8 +382,8 @@ __global__ void __launch_bounds__(kThreads, 1)
     } else {
       if (c < q_chunks) {  // stage s was last read by chunk c - 2, whose MMAs have completed
         const size_t chunk_id = (static_cast<size_t>(b) * Hkv + kvh) * (S / kKeys) + c;
-        dequant_kivi_tile(kivi + chunk_id * kivi_chunk_bytes(kivi_bits), kivi_bits, k_tiles + s * kTile,
-                          v_tiles + s * kTile, tid);
+        dequant_kivi_tile(kivi + chunk_id * kivi_chunk_bytes(kivi_bits), kivi_bits, k_tiles + s * kKVTile,
+                          v_tiles + s * kKVTile, tid);
         fence_async_smem();
         tc_fence_before();
         __syncthreads();
@@ -374,9 +391,9 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
     if (tid == 0) {
       tc_fence_after();
-      const uint32_t qa = smem_u32(q_tile), ka = smem_u32(k_tiles + (FP8 ? 0 : s * kTile));
+      const uint32_t qa = smem_u32(q_tile), ka = smem_u32(k_tiles + (FP8 ? 0 : s * kKVTile));
 #pragma unroll
-      for (int kk = 0; kk < kDim / 16; ++kk) {
+      for (int kk = 0; kk < D / 16; ++kk) {
         const uint32_t off = (kk >> 2) * kAtom + (kk & 3) * 32;
         umma_bf16(tmem, desc_kmajor_sw128(qa + off), desc_kmajor_sw128(ka + off), idesc_s, kk != 0);
       }
@@ -443,7 +460,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
     if (tid == 0) {
       tc_fence_after();
-      const uint32_t pa = smem_u32(p_tile), va = smem_u32(v_tiles + (FP8 ? 0 : s * kTile));
+      const uint32_t pa = smem_u32(p_tile), va = smem_u32(v_tiles + (FP8 ? 0 : s * kKVTile));
 #pragma unroll
       for (int kk = 0; kk < kKeys / 16; ++kk) {
         const uint32_t a_off = (kk >> 2) * kAtom + (kk & 3) * 32;
@@ -460,11 +477,11 @@ __global__ void __launch_bounds__(kThreads, 1)
     if (stamp && i == 0) stamp[5] = global_timer_ns();
     if (!FP8 && tid == 0 && c_after < c1) issue_kv(c_after, s);  // both MMAs reading stage s are done
     __syncwarp();
-    float pv[32];
-    tmem_ld16(tmem_pv + lane_off, pv);
-    tmem_ld16(tmem_pv + lane_off + 16, pv + 16);
+    float pv[kDQ];
 #pragma unroll
-    for (int d = 0; d < 32; ++d) o[d] = o[d] * alpha + pv[d];
+    for (int c16 = 0; c16 < kDQ; c16 += 16) tmem_ld16(tmem_pv + lane_off + c16, pv + c16);
+#pragma unroll
+    for (int d = 0; d < kDQ; ++d) o[d] = o[d] * alpha + pv[d];
     c = c_next;
     c_next = c_after;
   }
@@ -479,7 +496,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   if constexpr (FP8) {  // O = s_v * (P . V8)
     const float sv = v_scale[kvh];
 #pragma unroll
-    for (int d = 0; d < 32; ++d) o[d] *= sv;
+    for (int d = 0; d < kDQ; ++d) o[d] *= sv;
   }
 
   if (!failed && row_valid) {
@@ -487,9 +504,9 @@ __global__ void __launch_bounds__(kThreads, 1)
       if (lse_out != nullptr && quarter == 0)  // log2-domain log-sum-exp of the row's scaled scores
         lse_out[(static_cast<size_t>(b) * T + t) * H + head] = l_tot > 0.f ? m_run + __log2f(l_tot) : -INFINITY;
       const float inv = l_tot > 0.f ? 1.f / l_tot : 0.f;
-      uint4* dst = reinterpret_cast<uint4*>(out + ((static_cast<size_t>(b) * T + t) * H + head) * kDim + col0);
+      uint4* dst = reinterpret_cast<uint4*>(out + ((static_cast<size_t>(b) * T + t) * H + head) * D + ocol0);
 #pragma unroll
-      for (int c = 0; c < 4; ++c) {
+      for (int c = 0; c < kDQ / 8; ++c) {
         uint32_t w[4];
 #pragma unroll
         for (int u = 0; u < 4; ++u) {
@@ -500,9 +517,9 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
     } else {
       const size_t slot = (static_cast<size_t>(blockIdx.x) * splits + split) * kRows + r;
-      float4* dst = reinterpret_cast<float4*>(ws_o + slot * kDim + col0);
+      float4* dst = reinterpret_cast<float4*>(ws_o + slot * D + ocol0);
 #pragma unroll
-      for (int c = 0; c < 8; ++c) dst[c] = make_float4(o[4 * c], o[4 * c + 1], o[4 * c + 2], o[4 * c + 3]);
+      for (int c = 0; c < kDQ / 4; ++c) dst[c] = make_float4(o[4 * c], o[4 * c + 1], o[4 * c + 2], o[4 * c + 3]);
       if (quarter == 0) {
         ws_ml[slot * 2] = m_run;
         ws_ml[slot * 2 + 1] = l_tot;
@@ -515,47 +532,52 @@ __global__ void __launch_bounds__(kThreads, 1)
 
 // Merge of the split partials, one warp per packed row (a launch of its own: one warp per row keeps the chains of
 // dependent loads short, where a last-arriving CTA merging all 128 rows was measured 3x slower).
+template <int D>
 __global__ void __launch_bounds__(128) attn_merge_kernel(const float* __restrict__ ws_o,
                                                          const float* __restrict__ ws_ml, bf16* __restrict__ out,
                                                          int T, int H, int Hkv, int m_tiles, int splits,
                                                          float* __restrict__ lse_out) {
   pdl_trigger();
   pdl_wait();
-  merge_row(ws_o, ws_ml, out, blockIdx.x, blockIdx.y * 4 + (threadIdx.x >> 5), threadIdx.x & 31, T, H, Hkv, m_tiles,
+  merge_row<D>(ws_o, ws_ml, out, blockIdx.x, blockIdx.y * 4 + (threadIdx.x >> 5), threadIdx.x & 31, T, H, Hkv, m_tiles,
             splits, lse_out);
 }
 
 // Exact-tail merge: one warp per packed row combines the tensor-core partials of every split with the row's tail
-// keys (positions [p - tail_w, p]), which it attends itself in position order. Lane l owns dimensions 4l .. 4l + 3;
-// a score is the lane products summed in a fixed order and then over the warp by a butterfly, so every lane holds
-// the same value, and it is computed the same way in both passes over the tail (max, then weights).
-__device__ __forceinline__ float4 load_kv4(const uint8_t* base, size_t row, int lane, bool fp8) {
-  if (fp8) {
-    const uint32_t w = *reinterpret_cast<const uint32_t*>(base + row * kDim + lane * 4);
-    float4 v;
+// keys (positions [p - tail_w, p]), which it attends itself in position order. Lane l owns dimensions E l .. E l + E
+// - 1 (E = D / 32); a score is the lane products summed in a fixed order and then over the warp by a butterfly, so
+// every lane holds the same value, and it is computed the same way in both passes over the tail (max, then weights).
+template <int E>
+__device__ __forceinline__ void load_kv(const uint8_t* base, size_t row, int lane, bool fp8, float* v) {
+  if (fp8) {  // e4m3 codes (head dimension 128, E = 4)
+    const uint32_t w = *reinterpret_cast<const uint32_t*>(base + row * (32 * E) + lane * E);
     const __half2 lo = __half2(__nv_cvt_fp8x2_to_halfraw2(static_cast<__nv_fp8x2_storage_t>(w & 0xFFFFu), __NV_E4M3));
     const __half2 hi = __half2(__nv_cvt_fp8x2_to_halfraw2(static_cast<__nv_fp8x2_storage_t>(w >> 16), __NV_E4M3));
     const float2 a = __half22float2(lo), b = __half22float2(hi);
-    v.x = a.x; v.y = a.y; v.z = b.x; v.w = b.y;
-    return v;
+    v[0] = a.x; v[1] = a.y; v[2] = b.x; v[3] = b.y;
+    return;
   }
-  const uint2 w = *reinterpret_cast<const uint2*>(base + (row * kDim + lane * 4) * 2);
-  const float2 a = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&w.x));
-  const float2 b = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&w.y));
-  return make_float4(a.x, a.y, b.x, b.y);
+  const __nv_bfloat162* src = reinterpret_cast<const __nv_bfloat162*>(base + (row * (32 * E) + lane * E) * 2);
+#pragma unroll
+  for (int e = 0; e < E; e += 2) {
+    const float2 f = __bfloat1622float2(src[e / 2]);
+    v[e] = f.x;
+    v[e + 1] = f.y;
+  }
 }
 
-__device__ __forceinline__ float tail_score(const float4& qv, const float4& kv, float scale_log2) {
-  float d = qv.x * kv.x;
-  d = fmaf(qv.y, kv.y, d);
-  d = fmaf(qv.z, kv.z, d);
-  d = fmaf(qv.w, kv.w, d);
+template <int E>
+__device__ __forceinline__ float tail_score(const float* qv, const float* kv, float scale_log2) {
+  float d = qv[0] * kv[0];
+#pragma unroll
+  for (int e = 1; e < E; ++e) d = fmaf(qv[e], kv[e], d);
   return warp_sum(d) * scale_log2;
 }
 
 constexpr int kTailKeysMax = 128;  // committed tail (tail_w <= 64) + new keys (at most 64)
 constexpr int kTailBatch = 8;      // keys whose loads are issued together
 
+template <int D>
 __global__ void __launch_bounds__(128) attn_merge_tail_kernel(
     const float* __restrict__ ws_o, const float* __restrict__ ws_ml, bf16* __restrict__ out, int T, int H, int Hkv,
     int m_tiles, int splits, float* __restrict__ lse_out, const bf16* __restrict__ q,
@@ -585,8 +607,9 @@ __global__ void __launch_bounds__(128) attn_merge_tail_kernel(
   const int depth = max(0, use_mask ? (__popcll(bits) - 1) : (q_offset + t));  // a row seeing no new key: 0
   const int lo = max(0, base + depth - tail_w);
   const size_t row0 = (static_cast<size_t>(b) * Hkv + kvh) * S;
-  const float4 qv = load_kv4(reinterpret_cast<const uint8_t*>(q),
-                             (static_cast<size_t>(b) * T + t) * H + head, lane, false);
+  constexpr int E = D / 32;
+  float qv[E];
+  load_kv<E>(reinterpret_cast<const uint8_t*>(q), (static_cast<size_t>(b) * T + t) * H + head, lane, false, qv);
   const int n_end = min(nn, use_mask ? 64 : q_offset + t + 1);
 
   // the tail keys in position order: committed slots [lo, base) the keep bitmap shows, then the row's own new keys
@@ -617,14 +640,14 @@ __global__ void __launch_bounds__(128) attn_merge_tail_kernel(
     if (ws_ml[slot * 2 + 1] > 0.f) mx = fmaxf(mx, ws_ml[slot * 2]);
   }
   for (int i0 = 0; i0 < n_keys; i0 += kTailBatch) {
-    float4 kv[kTailBatch];
+    float kv[kTailBatch][E];
 #pragma unroll
     for (int u = 0; u < kTailBatch; ++u)
-      if (i0 + u < n_keys) kv[u] = load_kv4(k_cache, row0 + s_row[wid][i0 + u], lane, fp8);
+      if (i0 + u < n_keys) load_kv<E>(k_cache, row0 + s_row[wid][i0 + u], lane, fp8, kv[u]);
 #pragma unroll
     for (int u = 0; u < kTailBatch; ++u) {
       if (i0 + u < n_keys) {
-        const float sc = tail_score(qv, kv[u], sl);
+        const float sc = tail_score<E>(qv, kv[u], sl);
         if (lane == 0) s_sc[wid][i0 + u] = sc;
         mx = fmaxf(mx, sc);
       }
@@ -633,29 +656,31 @@ __global__ void __launch_bounds__(128) attn_merge_tail_kernel(
   __syncwarp();
 
   // the splits' partials, then the tail keys in position order
-  float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+  float acc[E];
+#pragma unroll
+  for (int e = 0; e < E; ++e) acc[e] = 0.f;
   float denom = 0.f;
   for (int sp = 0; sp < splits; ++sp) {
     const size_t slot = (static_cast<size_t>(tile) * splits + sp) * kRows + r;
     const float l = ws_ml[slot * 2 + 1];
     if (!(l > 0.f)) continue;
     const float w = exp2f(ws_ml[slot * 2] - mx);
-    const float4 v = reinterpret_cast<const float4*>(ws_o + slot * kDim)[lane];
-    acc.x += v.x * w; acc.y += v.y * w; acc.z += v.z * w; acc.w += v.w * w;
+    const float* v = ws_o + slot * D + lane * E;
+#pragma unroll
+    for (int e = 0; e < E; ++e) acc[e] += v[e] * w;
     denom += l * w;
   }
   for (int i0 = 0; i0 < n_keys; i0 += kTailBatch) {
-    float4 vv[kTailBatch];
+    float vv[kTailBatch][E];
 #pragma unroll
     for (int u = 0; u < kTailBatch; ++u)
-      if (i0 + u < n_keys) vv[u] = load_kv4(v_cache, row0 + s_row[wid][i0 + u], lane, fp8);
+      if (i0 + u < n_keys) load_kv<E>(v_cache, row0 + s_row[wid][i0 + u], lane, fp8, vv[u]);
 #pragma unroll
     for (int u = 0; u < kTailBatch; ++u) {
       if (i0 + u < n_keys) {
         const float w = exp2f(s_sc[wid][i0 + u] - mx);
-        float4 v = vv[u];
-        v.x *= sv; v.y *= sv; v.z *= sv; v.w *= sv;
-        acc.x += v.x * w; acc.y += v.y * w; acc.z += v.z * w; acc.w += v.w * w;
+#pragma unroll
+        for (int e = 0; e < E; ++e) acc[e] += (vv[u][e] * sv) * w;
         denom += w;
       }
     }
@@ -664,9 +689,10 @@ __global__ void __launch_bounds__(128) attn_merge_tail_kernel(
   const float inv = denom > 0.f ? 1.f / denom : 0.f;
   if (lse_out != nullptr && lane == 0)
     lse_out[(static_cast<size_t>(b) * T + t) * H + head] = denom > 0.f ? mx + __log2f(denom) : -INFINITY;
-  bf16* dst = out + ((static_cast<size_t>(b) * T + t) * H + head) * kDim + lane * 4;
-  *reinterpret_cast<__nv_bfloat162*>(dst) = __floats2bfloat162_rn(acc.x * inv, acc.y * inv);
-  *reinterpret_cast<__nv_bfloat162*>(dst + 2) = __floats2bfloat162_rn(acc.z * inv, acc.w * inv);
+  bf16* dst = out + ((static_cast<size_t>(b) * T + t) * H + head) * D + lane * E;
+#pragma unroll
+  for (int e = 0; e < E; e += 2)
+    *reinterpret_cast<__nv_bfloat162*>(dst + e) = __floats2bfloat162_rn(acc[e] * inv, acc[e + 1] * inv);
 }
 
 // ---- attention scores for KV eviction (H2O / SnapKV / PyramidKV) -------------------------------------------------
@@ -867,7 +893,7 @@ __global__ void kivi_advance_kernel(const int* __restrict__ kv_len, int* __restr
 
 // The split over keys depends on the batch, the KV heads and the cache size only (not on the number of query
 // tokens), so a one-token pass and a verification pass reduce a row's keys in the same order.
-AttnPlan attention_plan(int B, int T, int H, int Hkv, int S, int num_sms, bool tail) {
+AttnPlan attention_plan(int B, int T, int H, int Hkv, int S, int num_sms, bool tail, int D) {
   AttnPlan plan;
   const int G = H / Hkv;
   plan.m_tiles = (T * G + kRows - 1) / kRows;
@@ -878,7 +904,7 @@ AttnPlan attention_plan(int B, int T, int H, int Hkv, int S, int num_sms, bool t
   plan.chunks_per_split = (total_chunks + splits - 1) / splits;
   plan.splits = (total_chunks + plan.chunks_per_split - 1) / plan.chunks_per_split;
   const long ctas = static_cast<long>(heads) * plan.m_tiles;
-  plan.ws_floats = (plan.splits > 1 || tail) ? ctas * plan.splits * kRows * (kDim + 2) : 0;
+  plan.ws_floats = (plan.splits > 1 || tail) ? ctas * plan.splits * kRows * (D + 2) : 0;
   plan.tail = tail;
   return plan;
 }
@@ -892,31 +918,38 @@ int launch_attention(const void* q, const CUtensorMap* tm_k, const CUtensorMap* 
   if (kivi != nullptr && (k_scale != nullptr || (kivi_bits != 2 && kivi_bits != 4))) return -1;
   if (tail_w < 0 || tail_w > 64 || (tail_w > 0 && (!plan.tail || k_cache == nullptr || v_cache == nullptr)))
     return -1;
-  if (D != kDim || H % Hkv != 0) return -1;
+  if ((D != 64 && D != 128) || H % Hkv != 0) return -1;
   if (mask != nullptr && T > 64) return -1;
   const bool fp8 = k_scale != nullptr;
   if (fp8 && v_scale == nullptr) return -1;
-  set_max_smem(attn_tc_kernel<false>, kSmem);
-  set_max_smem(attn_tc_kernel<true>, kSmem);
+  if (D != 128 && (fp8 || kivi != nullptr)) return -1;  // fp8 and KIVI caches at head dimension 128
   const int ctas = B * Hkv * plan.m_tiles;
   const bool staged = plan.splits > 1 || tail_w > 0;  // partials go through the workspace and a merge
   float* ws_o = staged ? ws : nullptr;
-  float* ws_ml = staged ? ws + static_cast<size_t>(ctas) * plan.splits * kRows * kDim : nullptr;
+  float* ws_ml = staged ? ws + static_cast<size_t>(ctas) * plan.splits * kRows * D : nullptr;
   dim3 grid(ctas, plan.splits);
-  launch_pdl(fp8 ? attn_tc_kernel<true> : attn_tc_kernel<false>, grid, dim3(kThreads), kSmem, stream,
-             static_cast<const bf16*>(q), *tm_k, *tm_v, static_cast<bf16*>(out), ws_o, ws_ml, kv_len, n_new, mask, T,
-             H, Hkv, S, scale * 1.4426950408889634f, q_offset, plan.chunks_per_split, plan.m_tiles, status, trace,
-             k_scale, v_scale, keep, lse_out, kivi, kivi_chunks, kivi_bits, tail_w);
+  const float sl2 = scale * 1.4426950408889634f;
+  auto run = [&](auto kernel, int smem) {
+    set_max_smem(kernel, smem);
+    launch_pdl(kernel, grid, dim3(kThreads), smem, stream, static_cast<const bf16*>(q), *tm_k, *tm_v,
+               static_cast<bf16*>(out), ws_o, ws_ml, kv_len, n_new, mask, T, H, Hkv, S, sl2, q_offset,
+               plan.chunks_per_split, plan.m_tiles, status, trace, k_scale, v_scale, keep, lse_out, kivi, kivi_chunks,
+               kivi_bits, tail_w);
+  };
+  if (D == 64) run(attn_tc_kernel<false, 64>, attn_smem_bytes(64));
+  else if (fp8) run(attn_tc_kernel<true, 128>, kSmem);
+  else run(attn_tc_kernel<false, 128>, kSmem);
+  dim3 mgrid(ctas, kRows / 4);
   if (tail_w > 0) {
-    dim3 mgrid(ctas, kRows / 4);
-    launch_pdl(attn_merge_tail_kernel, mgrid, dim3(128), 0, stream, static_cast<const float*>(ws_o),
+    auto merge = D == 64 ? attn_merge_tail_kernel<64> : attn_merge_tail_kernel<128>;
+    launch_pdl(merge, mgrid, dim3(128), 0, stream, static_cast<const float*>(ws_o),
                static_cast<const float*>(ws_ml), static_cast<bf16*>(out), T, H, Hkv, plan.m_tiles, plan.splits,
                lse_out, static_cast<const bf16*>(q), static_cast<const uint8_t*>(k_cache),
-               static_cast<const uint8_t*>(v_cache), kv_len, n_new, mask, S, scale * 1.4426950408889634f, q_offset,
-               tail_w, k_scale, v_scale, keep);
+               static_cast<const uint8_t*>(v_cache), kv_len, n_new, mask, S, sl2, q_offset, tail_w, k_scale, v_scale,
+               keep);
   } else if (plan.splits > 1) {
-    dim3 mgrid(ctas, kRows / 4);
-    launch_pdl(attn_merge_kernel, mgrid, dim3(128), 0, stream, static_cast<const float*>(ws_o),
+    auto merge = D == 64 ? attn_merge_kernel<64> : attn_merge_kernel<128>;
+    launch_pdl(merge, mgrid, dim3(128), 0, stream, static_cast<const float*>(ws_o),
                static_cast<const float*>(ws_ml), static_cast<bf16*>(out), T, H, Hkv, plan.m_tiles, plan.splits,
                lse_out);
   }

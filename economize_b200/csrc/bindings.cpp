@@ -186,7 +186,7 @@ Tensor rope_store(Tensor qkv, Tensor positions, Tensor cos, Tensor sin, int64_t 
                   c10::optional<Tensor> k_norm, double eps, int64_t q_offset, c10::optional<Tensor> k_scale,
                   c10::optional<Tensor> v_scale) {
   CHECK_CUDA(qkv);
-  TORCH_CHECK(D == 128, "rope_store: head_dim must be 128, got ", D);
+  TORCH_CHECK(D == 64 || D == 128 || D == 256, "rope_store: head_dim must be 64, 128 or 256, got ", D);
   const auto [qkv_splits, qkv_shape] = parts_of(qkv);
   const bool fp8 = fp8_cache(k_cache, k_scale, v_scale, Hkv);
   TORCH_CHECK(v_cache.scalar_type() == k_cache.scalar_type(), "K and V caches must share a dtype");
@@ -227,7 +227,8 @@ Tensor attention(Tensor q, Tensor k_cache, Tensor v_cache, Tensor kv_len, Tensor
                  c10::optional<Tensor> kivi, c10::optional<Tensor> kivi_chunks, int64_t kivi_bits, int64_t tail) {
   CHECK_CUDA(q);
   CHECK_BF16(q);
-  TORCH_CHECK(q.dim() == 4 && q.size(3) == 128 && k_cache.dim() == 4, "attention: head_dim must be 128");
+  TORCH_CHECK(q.dim() == 4 && (q.size(3) == 128 || q.size(3) == 64) && k_cache.dim() == 4,
+              "attention: head_dim must be 64 or 128");
   TORCH_CHECK(tail >= 0 && tail <= 64, "attention: the exact tail covers 0 .. 64 positions");
   const bool fp8 = fp8_cache(k_cache, k_scale, v_scale, k_cache.size(1));
   TORCH_CHECK(v_cache.scalar_type() == k_cache.scalar_type(), "K and V caches must share a dtype");
@@ -276,7 +277,8 @@ Tensor attention(Tensor q, Tensor k_cache, Tensor v_cache, Tensor kv_len, Tensor
   }
   auto out = at::empty_like(q);
   if (tail > 0) TORCH_CHECK(T <= 64, "attention: the exact tail serves passes of at most 64 query tokens");
-  const ecz::AttnPlan plan = ecz::attention_plan(B, T, H, Hkv, S, num_sms(q.get_device()), tail > 0);
+  TORCH_CHECK(k_cache.size(3) == D && v_cache.size(3) == D, "attention: caches must have q's head_dim");
+  const ecz::AttnPlan plan = ecz::attention_plan(B, T, H, Hkv, S, num_sms(q.get_device()), tail > 0, D);
   Tensor ws;
   if (plan.ws_floats > 0) ws = at::empty({plan.ws_floats}, q.options().dtype(at::kFloat));
   const uint64_t rows = static_cast<uint64_t>(B) * Hkv * S;
@@ -302,7 +304,8 @@ Tensor attention(Tensor q, Tensor k_cache, Tensor v_cache, Tensor kv_len, Tensor
                                        kivi.has_value() ? kivi_chunks->data_ptr<int>() : nullptr,
                                        static_cast<int>(kivi_bits), static_cast<int>(tail), k_cache.data_ptr(),
                                        v_cache.data_ptr());
-  TORCH_CHECK(rc == 0, "attention: unsupported shape (head_dim must be 128, H divisible by H_kv)");
+  TORCH_CHECK(rc == 0, "attention: unsupported shape (head_dim 64 or 128, fp8 and KIVI caches at 128, H divisible "
+              "by H_kv)");
   return out;
 }
 

@@ -162,6 +162,7 @@ int launch_rmsnorm(const void* x, const void* resid, const void* w, void* out, v
 // qkv [B*T, (H + 2 Hkv) * D]; q_out [B*T, H, D]; caches [B, Hkv, S, D]; token (b, t) writes slot
 // kv_len[b] + q_offset + t when q_offset + t < n_new[b]. One warp per (token, head slot), head slot in
 // [0, H + Hkv): q heads first, then kv heads (k rotated and stored with its v).
+template <int D>
 __global__ void __launch_bounds__(256) rope_store_kernel(
     const bf16* __restrict__ qkv, const int* __restrict__ positions, const float* __restrict__ cos_t,
     const float* __restrict__ sin_t, bf16* __restrict__ q_out, bf16* __restrict__ k_cache,
@@ -170,7 +171,7 @@ __global__ void __launch_bounds__(256) rope_store_kernel(
     int S, int q_offset, const float* __restrict__ k_scale, const float* __restrict__ v_scale, Parts parts) {
   pdl_trigger();
   pdl_wait();
-  constexpr int D = 128;
+  constexpr int E = D / 64;  // elements per lane in each half of the head (pairs of E / 2)
   const int warp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
   const int lane = threadIdx.x & 31;
   const int slots = H + Hkv;
@@ -181,35 +182,46 @@ __global__ void __launch_bounds__(256) rope_store_kernel(
   const bool is_q = head < H;
   const int width = (H + 2 * Hkv) * D;
   const size_t src = static_cast<size_t>(token) * width + (is_q ? head * D : H * D + (head - H) * D);
-  // lane owns elements (2*lane, 2*lane+1) of the first half and their partners in the second half
-  const int i0 = 2 * lane;
-  __nv_bfloat162 lo = load2(qkv, parts, src + i0);
-  __nv_bfloat162 hi = load2(qkv, parts, src + i0 + D / 2);
-  float x0 = __bfloat162float(lo.x), x1 = __bfloat162float(lo.y);
-  float y0 = __bfloat162float(hi.x), y1 = __bfloat162float(hi.y);
+  // lane owns elements [E * lane, E * lane + E) of the first half and their partners in the second half
+  const int i0 = E * lane;
+  float x[E], y[E];
+#pragma unroll
+  for (int e = 0; e < E; e += 2) {
+    const __nv_bfloat162 lo = load2(qkv, parts, src + i0 + e);
+    const __nv_bfloat162 hi = load2(qkv, parts, src + i0 + e + D / 2);
+    x[e] = __bfloat162float(lo.x); x[e + 1] = __bfloat162float(lo.y);
+    y[e] = __bfloat162float(hi.x); y[e + 1] = __bfloat162float(hi.y);
+  }
   const bf16* nw = is_q ? q_norm : k_norm;
   if (nw != nullptr) {
-    float ss = warp_sum(x0 * x0 + x1 * x1 + y0 * y0 + y1 * y1);
-    const float inv = rsqrtf(ss / D + eps);
-    x0 = __bfloat162float(nw[i0]) * bf16r(x0 * inv);
-    x1 = __bfloat162float(nw[i0 + 1]) * bf16r(x1 * inv);
-    y0 = __bfloat162float(nw[i0 + D / 2]) * bf16r(y0 * inv);
-    y1 = __bfloat162float(nw[i0 + D / 2 + 1]) * bf16r(y1 * inv);
-    x0 = bf16r(x0); x1 = bf16r(x1); y0 = bf16r(y0); y1 = bf16r(y1);
+    float part = 0.f;
+#pragma unroll
+    for (int e = 0; e < E; ++e) part += x[e] * x[e] + y[e] * y[e];
+    const float inv = rsqrtf(warp_sum(part) / D + eps);
+#pragma unroll
+    for (int e = 0; e < E; ++e) {
+      x[e] = bf16r(__bfloat162float(nw[i0 + e]) * bf16r(x[e] * inv));
+      y[e] = bf16r(__bfloat162float(nw[i0 + e + D / 2]) * bf16r(y[e] * inv));
+    }
   }
   const int pos = positions[token];
   const float* cp = cos_t + static_cast<size_t>(pos) * (D / 2) + i0;
   const float* sp = sin_t + static_cast<size_t>(pos) * (D / 2) + i0;
-  const float c0 = bf16r(cp[0]), c1 = bf16r(cp[1]), s0 = bf16r(sp[0]), s1 = bf16r(sp[1]);
   // out = x * cos + rotate_half(x) * sin, each product rounded to bf16 (HF computes it in the input dtype)
-  const float r0 = bf16r(bf16r(x0 * c0) + bf16r(-y0 * s0));
-  const float r1 = bf16r(bf16r(x1 * c1) + bf16r(-y1 * s1));
-  const float r2 = bf16r(bf16r(y0 * c0) + bf16r(x0 * s0));
-  const float r3 = bf16r(bf16r(y1 * c1) + bf16r(x1 * s1));
+  float ra[E], rb[E];
+#pragma unroll
+  for (int e = 0; e < E; ++e) {
+    const float c = bf16r(cp[e]), sn = bf16r(sp[e]);
+    ra[e] = bf16r(bf16r(x[e] * c) + bf16r(-y[e] * sn));
+    rb[e] = bf16r(bf16r(y[e] * c) + bf16r(x[e] * sn));
+  }
   if (is_q) {
     bf16* dst = q_out + (static_cast<size_t>(token) * H + head) * D;
-    *reinterpret_cast<__nv_bfloat162*>(dst + i0) = __floats2bfloat162_rn(r0, r1);
-    *reinterpret_cast<__nv_bfloat162*>(dst + i0 + D / 2) = __floats2bfloat162_rn(r2, r3);
+#pragma unroll
+    for (int e = 0; e < E; e += 2) {
+      *reinterpret_cast<__nv_bfloat162*>(dst + i0 + e) = __floats2bfloat162_rn(ra[e], ra[e + 1]);
+      *reinterpret_cast<__nv_bfloat162*>(dst + i0 + e + D / 2) = __floats2bfloat162_rn(rb[e], rb[e + 1]);
+    }
     return;
   }
   const int j = q_offset + t;
@@ -217,9 +229,9 @@ __global__ void __launch_bounds__(256) rope_store_kernel(
   const int kvh = head - H;
   const size_t slot = static_cast<size_t>(kv_len[b]) + j;
   const size_t off = ((static_cast<size_t>(b) * Hkv + kvh) * S + slot) * D;
+  const size_t vsrc = static_cast<size_t>(token) * width + (H + Hkv) * D + kvh * D;
   if (k_scale != nullptr) {
     // fp8 cache: e4m3 codes of value / scale (quotient rounded to fp32 first, then to e4m3 with saturation)
-    const size_t vsrc = static_cast<size_t>(token) * width + (H + Hkv) * D + kvh * D;
     const float sk = k_scale[kvh], sv = v_scale[kvh];
     uint8_t* kc = reinterpret_cast<uint8_t*>(k_cache) + off;
     uint8_t* vc = reinterpret_cast<uint8_t*>(v_cache) + off;
@@ -227,19 +239,24 @@ __global__ void __launch_bounds__(256) rope_store_kernel(
       *reinterpret_cast<__nv_fp8x2_storage_t*>(dst) =
           __nv_cvt_float2_to_fp8x2(make_float2(a, b2), __NV_SATFINITE, __NV_E4M3);
     };
-    put(kc + i0, __fdiv_rn(bf16r(r0), sk), __fdiv_rn(bf16r(r1), sk));
-    put(kc + i0 + D / 2, __fdiv_rn(bf16r(r2), sk), __fdiv_rn(bf16r(r3), sk));
-    const __nv_bfloat162 va = load2(qkv, parts, vsrc + i0);
-    const __nv_bfloat162 vb = load2(qkv, parts, vsrc + i0 + D / 2);
-    put(vc + i0, __fdiv_rn(__bfloat162float(va.x), sv), __fdiv_rn(__bfloat162float(va.y), sv));
-    put(vc + i0 + D / 2, __fdiv_rn(__bfloat162float(vb.x), sv), __fdiv_rn(__bfloat162float(vb.y), sv));
+#pragma unroll
+    for (int e = 0; e < E; e += 2) {
+      put(kc + i0 + e, __fdiv_rn(ra[e], sk), __fdiv_rn(ra[e + 1], sk));
+      put(kc + i0 + e + D / 2, __fdiv_rn(rb[e], sk), __fdiv_rn(rb[e + 1], sk));
+      const __nv_bfloat162 va = load2(qkv, parts, vsrc + i0 + e);
+      const __nv_bfloat162 vb = load2(qkv, parts, vsrc + i0 + e + D / 2);
+      put(vc + i0 + e, __fdiv_rn(__bfloat162float(va.x), sv), __fdiv_rn(__bfloat162float(va.y), sv));
+      put(vc + i0 + e + D / 2, __fdiv_rn(__bfloat162float(vb.x), sv), __fdiv_rn(__bfloat162float(vb.y), sv));
+    }
     return;
   }
-  *reinterpret_cast<__nv_bfloat162*>(k_cache + off + i0) = __floats2bfloat162_rn(r0, r1);
-  *reinterpret_cast<__nv_bfloat162*>(k_cache + off + i0 + D / 2) = __floats2bfloat162_rn(r2, r3);
-  const size_t vsrc = static_cast<size_t>(token) * width + (H + Hkv) * D + kvh * D;
-  *reinterpret_cast<__nv_bfloat162*>(v_cache + off + i0) = load2(qkv, parts, vsrc + i0);
-  *reinterpret_cast<__nv_bfloat162*>(v_cache + off + i0 + D / 2) = load2(qkv, parts, vsrc + i0 + D / 2);
+#pragma unroll
+  for (int e = 0; e < E; e += 2) {
+    *reinterpret_cast<__nv_bfloat162*>(k_cache + off + i0 + e) = __floats2bfloat162_rn(ra[e], ra[e + 1]);
+    *reinterpret_cast<__nv_bfloat162*>(k_cache + off + i0 + e + D / 2) = __floats2bfloat162_rn(rb[e], rb[e + 1]);
+    *reinterpret_cast<__nv_bfloat162*>(v_cache + off + i0 + e) = load2(qkv, parts, vsrc + i0 + e);
+    *reinterpret_cast<__nv_bfloat162*>(v_cache + off + i0 + e + D / 2) = load2(qkv, parts, vsrc + i0 + e + D / 2);
+  }
 }
 
 int launch_rope_store(const void* qkv, const int* positions, const float* cos_t, const float* sin_t, void* q_out,
@@ -247,11 +264,12 @@ int launch_rope_store(const void* qkv, const int* positions, const float* cos_t,
                       const void* k_norm, float eps, int B, int T, int H, int Hkv, int D, int S, int q_offset,
                       cudaStream_t stream, const float* k_scale, const float* v_scale, const float* qkv_parts,
                       int splits) {
-  if (D != 128) return -1;
+  if (D != 64 && D != 128 && D != 256) return -1;
   const Parts parts{qkv_parts, splits, static_cast<long>(B) * T * (H + 2 * Hkv) * D};
   const long warps = static_cast<long>(B) * T * (H + Hkv);
   const int blocks = static_cast<int>((warps * 32 + 255) / 256);
-  launch_pdl(rope_store_kernel, dim3(blocks), dim3(256), 0, stream, static_cast<const bf16*>(qkv), positions, cos_t,
+  auto kernel = D == 64 ? rope_store_kernel<64> : D == 128 ? rope_store_kernel<128> : rope_store_kernel<256>;
+  launch_pdl(kernel, dim3(blocks), dim3(256), 0, stream, static_cast<const bf16*>(qkv), positions, cos_t,
              sin_t, static_cast<bf16*>(q_out), static_cast<bf16*>(k_cache), static_cast<bf16*>(v_cache), kv_len,
              n_new, static_cast<const bf16*>(q_norm), static_cast<const bf16*>(k_norm), eps, B * T, T, H, Hkv, S,
              q_offset, k_scale, v_scale, parts);

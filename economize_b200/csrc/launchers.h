@@ -102,7 +102,7 @@ int launch_gemm_persistent(const CUtensorMap* tm_w, const CUtensorMap* tm_x, voi
                            int N, int K, int num_sms, unsigned* status, cudaStream_t stream);
 
 // attention.cu
-AttnPlan attention_plan(int B, int T, int H, int Hkv, int S, int num_sms, bool tail = false);
+AttnPlan attention_plan(int B, int T, int H, int Hkv, int S, int num_sms, bool tail = false, int D = 128);
 int launch_attention(const void* q, const CUtensorMap* tm_k, const CUtensorMap* tm_v, void* out, float* ws,
                      const int* kv_len, const int* n_new, const int64_t* mask, int B, int T, int H, int Hkv, int D,
                      int S, float scale, int q_offset, const AttnPlan& plan, unsigned* status, cudaStream_t stream,

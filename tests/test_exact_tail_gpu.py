@@ -36,12 +36,12 @@ def _caches(fp8, B, Hkv, S, D, dev, g):
     return kq, vq, ks, vs
 
 
-@pytest.mark.parametrize("fp8", [False, True])
+@pytest.mark.parametrize("fp8,D", [(False, 128), (True, 128), (False, 64)])
 @pytest.mark.parametrize("base", [5, 250, 700])
-def test_tree_pass_equals_one_token_passes(cuda, fp8, base):
+def test_tree_pass_equals_one_token_passes(cuda, fp8, D, base):
     g = torch.Generator(device=cuda).manual_seed(base)
     gc = torch.Generator().manual_seed(base)
-    B, T, H, Hkv, S, D = 1, 61, 32, 8, 1024, 128
+    B, T, H, Hkv, S = 1, 61, 32, 8, 1024
     k, v, ks, vs = _caches(fp8, B, Hkv, S, D, cuda, g)
     q = torch.randn(B, T, H, D, device=cuda, generator=g).bfloat16()
     parents, bits = _tree(T, gc)
@@ -84,4 +84,41 @@ def test_tail_with_lse_and_causal(cuda):
     want = ops.attention(q, k, v, kv_len, n_new, None, lse_out=lse_ref)
     torch.testing.assert_close(out.float(), want.float(), atol=2e-2, rtol=2e-2)
     torch.testing.assert_close(lse, lse_ref, atol=1e-3, rtol=1e-4)
+    assert ops.require().status(0) == 0
+
+
+@pytest.mark.parametrize("T,lens", [(1, [300, 17]), (40, [129, 0]), (61, [700, 64])])
+def test_head_dim_64_attention(cuda, T, lens):
+    g = torch.Generator(device=cuda).manual_seed(T)
+    gc = torch.Generator().manual_seed(T)
+    B, H, Hkv, S, D = 2, 8, 2, 1024, 64
+    k = torch.randn(B, Hkv, S, D, device=cuda, generator=g).bfloat16()
+    v = torch.randn(B, Hkv, S, D, device=cuda, generator=g).bfloat16()
+    q = torch.randn(B, T, H, D, device=cuda, generator=g).bfloat16()
+    kv_len = torch.tensor(lens, dtype=torch.int32, device=cuda)
+    n_new = torch.full((B,), T, dtype=torch.int32, device=cuda)
+    mask = torch.tensor([_as_i64(_tree(T, gc)[1]) for _ in range(B)], device=cuda) if T > 1 else None
+    for tail in (0, 16):
+        out = ops.attention(q, k, v, kv_len, n_new, mask, tail=tail)
+        want = ref.attention(q.float(), k.float(), v.float(), kv_len, n_new, mask)
+        torch.testing.assert_close(out.float(), want.float(), atol=3e-2, rtol=3e-2)
+
+
+def test_head_dim_64_model_tree_equals_plain(cuda):
+    """A model with 64-dimensional heads (the Llama-3.2-1B / Qwen2.5-0.5B shape) through the engine."""
+    import economize_b200 as eco
+    from economize_b200.models.config import tiny_llama
+    from economize_b200.models.llama import CausalLM, init_weights
+    from economize_b200.techniques.eagle3 import Eagle3Config
+
+    cfg = tiny_llama(hidden_size=512, num_heads=8, num_kv_heads=2, head_dim=64, num_layers=3)
+    em = eco.apply(init_weights(CausalLM(cfg, torch.bfloat16, cuda), seed=0), Eagle3Config())
+    ps = [torch.randint(0, cfg.vocab_size, (n,), generator=torch.Generator().manual_seed(n)).to(cuda)
+          for n in (17, 140)]
+    plain = em.decode_batch(ps, 24, decoding=eco.DecodeConfig(cycle_length=1))
+    tree = em.decode_batch(ps, 24, decoding=eco.DecodeConfig(
+        cycle_length=7, draft_policy="dynamic_tree", draft_policy_options={"depth": 6, "topk": 10, "total_tokens": 60},
+        cuda_graphs=True))
+    for a, b in zip(plain, tree):
+        assert torch.equal(a.tokens, b.tokens)
     assert ops.require().status(0) == 0

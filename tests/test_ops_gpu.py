@@ -121,9 +121,10 @@ def test_attention_q_offset(cuda):
 
 
 @pytest.mark.parametrize("qk_norm", [False, True])
-def test_rope_store(cuda, qk_norm):
+@pytest.mark.parametrize("D", [64, 128, 256])
+def test_rope_store(cuda, qk_norm, D):
     g = torch.Generator(device=cuda).manual_seed(6)
-    B, T, H, Hkv, D, S = 2, 7, 8, 2, 128, 64
+    B, T, H, Hkv, S = 2, 7, 8, 2, 64
     qkv = torch.randn(B, T, (H + 2 * Hkv) * D, device=cuda, generator=g).bfloat16()
     pos = torch.randint(0, 40, (B, T), device=cuda, generator=g, dtype=torch.int32)
     inv = 1.0 / (10000 ** (torch.arange(0, D, 2, device=cuda).float() / D))
