@@ -18,9 +18,13 @@ from ..errors import UnsupportedModelError
 __all__ = ["ModelConfig", "SUPPORTED_MODEL_TYPES", "llama31_8b", "llama31_70b", "mixtral_8x7b", "rope_inv_freq",
            "tiny_llama"]
 
-#: ``model_type`` values whose decoder layer is the Llama block (pre-norm attention + gated MLP), with the
-#: differences expressed as fields: q/k/v bias (qwen2), per-head q/k RMSNorm (qwen3), sparse MoE MLP (mixtral).
-SUPPORTED_MODEL_TYPES = ("llama", "mistral", "qwen2", "qwen3", "mixtral", "economize_b200")
+#: ``model_type`` values whose decoder layer is the Llama block (attention + gated MLP with RMSNorms), with the
+#: differences expressed as fields: q/k/v bias (qwen2), per-head q/k RMSNorm (qwen3, qwen3_moe), sparse MoE MLP
+#: (mixtral, qwen3_moe), embedding / residual / attention / logit multipliers (granite), fused projections in the
+#: checkpoint (phi3), layers without rotary embedding (smollm3), norms after each branch and q/k RMSNorm over all
+#: heads (olmo2).
+SUPPORTED_MODEL_TYPES = ("llama", "mistral", "qwen2", "qwen3", "mixtral", "granite", "phi3", "smollm3", "olmo2",
+                         "qwen3_moe", "economize_b200")
 
 
 @dataclass
@@ -42,11 +46,26 @@ class ModelConfig:
     num_experts: int = 0
     experts_per_token: int = 2
     model_type: str = "llama"
+    #: top-k router weights renormalised to sum to one (Mixtral); False keeps the softmax probabilities (Qwen3-MoE)
+    norm_topk_prob: bool = True
+    #: scales of Granite: embeddings, each branch output before the residual add, attention logits (replaces
+    #: 1/sqrt(head_dim) when set), and a divisor of the LM head's logits
+    embedding_multiplier: float = 1.0
+    residual_multiplier: float = 1.0
+    attention_multiplier: float | None = None
+    logits_scaling: float = 1.0
+    #: OLMo-2 block: each branch's output is normed before it joins the residual stream (no input norms)
+    post_norm: bool = False
+    #: q/k RMSNorm over all heads' features at once (OLMo-2) instead of per head (Qwen3)
+    qk_norm_full: bool = False
+    #: layers whose attention runs without rotary embedding (SmolLM3's NoPE layers)
+    nope_layers: tuple[int, ...] = ()
     extra: dict[str, Any] = field(default_factory=dict)
 
     def __post_init__(self) -> None:
         if self.head_dim is None:
             self.head_dim = self.hidden_size // self.num_heads
+        self.nope_layers = tuple(int(i) for i in self.nope_layers)
         if self.num_heads % self.num_kv_heads:
             raise UnsupportedModelError(f"{self.num_heads} heads do not split into {self.num_kv_heads} KV groups")
 
@@ -86,16 +105,40 @@ class ModelConfig:
             raise UnsupportedModelError(f"model_type {model_type!r} is not supported; supported: "
                                         f"{', '.join(SUPPORTED_MODEL_TYPES)}")
         rope = get("rope_scaling") or get("rope_parameters")
+        if isinstance(rope, dict) and float(rope.get("partial_rotary_factor", 1.0)) != 1.0:
+            raise UnsupportedModelError(f"{model_type}: partial rotary embedding (factor "
+                                        f"{rope['partial_rotary_factor']}) is not supported")
+        if float(get("partial_rotary_factor", 1.0) or 1.0) != 1.0:
+            raise UnsupportedModelError(f"{model_type}: partial rotary embedding is not supported")
+        if get("use_sliding_window", False) or (get("sliding_window") and model_type not in ("mistral",)):
+            raise UnsupportedModelError(f"{model_type}: sliding-window attention layers are not supported")
         theta = get("rope_theta")
         if theta is None and isinstance(rope, dict):
             theta = rope.get("rope_theta")
         if isinstance(rope, dict) and rope.get("rope_type", rope.get("type", "default")) in ("default", None):
             rope = None
         heads = int(get("num_attention_heads"))
+        extra: dict[str, Any] = {}
+        experts = int(get("num_local_experts", 0) or get("num_experts", 0) or 0)
+        ffn = int(get("intermediate_size"))
+        if model_type == "qwen3_moe":
+            if int(get("decoder_sparse_step", 1) or 1) != 1 or list(get("mlp_only_layers", []) or []):
+                raise UnsupportedModelError("qwen3_moe with dense layers between the sparse ones is not supported")
+            ffn = int(get("moe_intermediate_size"))
+        if model_type == "smollm3":
+            flags = list(get("no_rope_layers", []) or [])
+            extra["nope_layers"] = tuple(i for i, use_rope in enumerate(flags) if not use_rope)
+        if model_type == "granite":
+            extra.update(embedding_multiplier=float(get("embedding_multiplier", 1.0)),
+                         residual_multiplier=float(get("residual_multiplier", 1.0)),
+                         attention_multiplier=float(get("attention_multiplier", 1.0)),
+                         logits_scaling=float(get("logits_scaling", 1.0)))
+        if model_type == "olmo2":
+            extra.update(post_norm=True, qk_norm_full=True)
         return cls(
             vocab_size=int(get("vocab_size")),
             hidden_size=int(get("hidden_size")),
-            intermediate_size=int(get("intermediate_size")),
+            intermediate_size=ffn,
             num_layers=int(get("num_hidden_layers")),
             num_heads=heads,
             num_kv_heads=int(get("num_key_value_heads") or heads),
@@ -106,10 +149,12 @@ class ModelConfig:
             max_position_embeddings=int(get("max_position_embeddings", 8192)),
             tie_word_embeddings=bool(get("tie_word_embeddings", False)),
             attention_bias=bool(get("attention_bias", model_type == "qwen2")),
-            qk_norm=model_type == "qwen3",
-            num_experts=int(get("num_local_experts", 0) or 0),
+            qk_norm=model_type in ("qwen3", "qwen3_moe", "olmo2"),
+            num_experts=experts,
             experts_per_token=int(get("num_experts_per_tok", 2) or 2),
             model_type=model_type,
+            norm_topk_prob=bool(get("norm_topk_prob", True)),
+            **extra,
         )
 
     def to_hf(self) -> Any:
@@ -124,10 +169,32 @@ class ModelConfig:
                       tie_word_embeddings=self.tie_word_embeddings, attention_bias=self.attention_bias)
         if self.rope_scaling is not None:
             common["rope_scaling"] = dict(self.rope_scaling)
+        kind = self.model_type
+        if kind == "qwen3_moe":
+            return transformers.Qwen3MoeConfig(num_experts=self.num_experts, num_experts_per_tok=self.experts_per_token,
+                                               moe_intermediate_size=self.intermediate_size,
+                                               norm_topk_prob=self.norm_topk_prob, **common)
         if self.is_moe:
             return transformers.MixtralConfig(num_local_experts=self.num_experts,
                                               num_experts_per_tok=self.experts_per_token,
                                               **{k: v for k, v in common.items() if k != "attention_bias"})
+        if kind == "granite":
+            return transformers.GraniteConfig(embedding_multiplier=self.embedding_multiplier,
+                                              residual_multiplier=self.residual_multiplier,
+                                              attention_multiplier=self.attention_multiplier or self.head_dim ** -0.5,
+                                              logits_scaling=self.logits_scaling, **common)
+        if kind == "phi3":
+            return transformers.Phi3Config(**{k: v for k, v in common.items() if k not in ("attention_bias",
+                                                                                            "head_dim")})
+        if kind == "smollm3":
+            flags = [0 if i in self.nope_layers else 1 for i in range(self.num_layers)]
+            return transformers.SmolLM3Config(no_rope_layers=flags, **common)
+        if kind == "olmo2":
+            return transformers.Olmo2Config(**{k: v for k, v in common.items() if k != "head_dim"})
+        if kind == "qwen3":
+            return transformers.Qwen3Config(**common)
+        if kind == "qwen2":
+            return transformers.Qwen2Config(**{k: v for k, v in common.items() if k != "attention_bias"})
         return transformers.LlamaConfig(**common)
 
 

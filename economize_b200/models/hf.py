@@ -31,15 +31,22 @@ def load_hf_state(model, state: dict[str, torch.Tensor]) -> None:
     for i, layer in enumerate(model.layers):
         p = f"model.layers.{i}."
         a = p + "self_attn."
-        layer.wqkv.copy_(torch.cat([_take(state, a + f"{n}_proj.weight") for n in "qkv"], 0))
+        if a + "qkv_proj.weight" in state:  # fused checkpoints (phi3): [q; k; v] rows already
+            layer.wqkv.copy_(state[a + "qkv_proj.weight"])
+        else:
+            layer.wqkv.copy_(torch.cat([_take(state, a + f"{n}_proj.weight") for n in "qkv"], 0))
         if layer.bqkv is not None:
             layer.bqkv.copy_(torch.cat([_take(state, a + f"{n}_proj.bias") for n in "qkv"], 0))
         layer.wo.copy_(_take(state, a + "o_proj.weight"))
         if layer.q_norm is not None:
             layer.q_norm.copy_(_take(state, a + "q_norm.weight"))
             layer.k_norm.copy_(_take(state, a + "k_norm.weight"))
-        layer.attn_norm.copy_(_take(state, p + "input_layernorm.weight"))
-        layer.mlp_norm.copy_(_take(state, p + "post_attention_layernorm.weight"))
+        if c.post_norm:  # olmo2: the norms follow the branches (attn_norm / mlp_norm hold them)
+            layer.attn_norm.copy_(_take(state, p + "post_attention_layernorm.weight"))
+            layer.mlp_norm.copy_(_take(state, p + "post_feedforward_layernorm.weight"))
+        else:
+            layer.attn_norm.copy_(_take(state, p + "input_layernorm.weight"))
+            layer.mlp_norm.copy_(_take(state, p + "post_attention_layernorm.weight"))
         if c.is_moe:
             if p + "mlp.experts.gate_up_proj" in state:
                 layer.router.copy_(_take(state, p + "mlp.gate.weight"))
@@ -55,8 +62,11 @@ def load_hf_state(model, state: dict[str, torch.Tensor]) -> None:
                     layer.w_down[e].copy_(_take(state, x + "w2.weight"))
         else:
             m = p + "mlp."
-            layer.w_gate_up.copy_(torch.cat([_take(state, m + "gate_proj.weight"),
-                                             _take(state, m + "up_proj.weight")], 0))
+            if m + "gate_up_proj.weight" in state:  # fused checkpoints (phi3): [gate; up]
+                layer.w_gate_up.copy_(state[m + "gate_up_proj.weight"])
+            else:
+                layer.w_gate_up.copy_(torch.cat([_take(state, m + "gate_proj.weight"),
+                                                 _take(state, m + "up_proj.weight")], 0))
             layer.w_down.copy_(_take(state, m + "down_proj.weight"))
 
 
@@ -78,9 +88,12 @@ def export_hf_state(model, copy: bool = True) -> dict[str, torch.Tensor]:
         out["lm_head.weight"] = model.lm_head.detach()
     for i, layer in enumerate(model.layers):
         p = f"model.layers.{i}."
-        q, k, v = full(layer.wqkv).split([c.q_size, c.kv_size, c.kv_size], 0)
-        for n, w in zip("qkv", (q, k, v)):
-            out[p + f"self_attn.{n}_proj.weight"] = w
+        if c.model_type == "phi3":
+            out[p + "self_attn.qkv_proj.weight"] = full(layer.wqkv)
+        else:
+            q, k, v = full(layer.wqkv).split([c.q_size, c.kv_size, c.kv_size], 0)
+            for n, w in zip("qkv", (q, k, v)):
+                out[p + f"self_attn.{n}_proj.weight"] = w
         if layer.bqkv is not None:
             for n, w in zip("qkv", layer.bqkv.detach().split([c.q_size, c.kv_size, c.kv_size], 0)):
                 out[p + f"self_attn.{n}_proj.bias"] = w
@@ -88,12 +101,19 @@ def export_hf_state(model, copy: bool = True) -> dict[str, torch.Tensor]:
         if layer.q_norm is not None:
             out[p + "self_attn.q_norm.weight"] = layer.q_norm.detach()
             out[p + "self_attn.k_norm.weight"] = layer.k_norm.detach()
-        out[p + "input_layernorm.weight"] = layer.attn_norm.detach()
-        out[p + "post_attention_layernorm.weight"] = layer.mlp_norm.detach()
+        if c.post_norm:
+            out[p + "post_attention_layernorm.weight"] = layer.attn_norm.detach()
+            out[p + "post_feedforward_layernorm.weight"] = layer.mlp_norm.detach()
+        else:
+            out[p + "input_layernorm.weight"] = layer.attn_norm.detach()
+            out[p + "post_attention_layernorm.weight"] = layer.mlp_norm.detach()
         if c.is_moe:
             out[p + "mlp.gate.weight"] = layer.router.detach()
             out[p + "mlp.experts.gate_up_proj"] = full(layer.w_gate_up)
             out[p + "mlp.experts.down_proj"] = full(layer.w_down)
+        elif c.model_type == "phi3":
+            out[p + "mlp.gate_up_proj.weight"] = full(layer.w_gate_up)
+            out[p + "mlp.down_proj.weight"] = full(layer.w_down)
         else:
             g, u = full(layer.w_gate_up).chunk(2, 0)
             out[p + "mlp.gate_proj.weight"] = g

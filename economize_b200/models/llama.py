@@ -42,8 +42,10 @@ class DecoderLayer(nn.Module):
         self.bqkv = nn.Parameter(torch.zeros(config.q_size + 2 * config.kv_size, **kw)) if config.attention_bias \
             else None
         self.wo = nn.Parameter(torch.empty(h, config.q_size, **kw))
-        self.q_norm = nn.Parameter(torch.ones(config.head_dim, **kw)) if config.qk_norm else None
-        self.k_norm = nn.Parameter(torch.ones(config.head_dim, **kw)) if config.qk_norm else None
+        # q/k RMSNorm weights: one head's width (per-head norm) or all heads' (a norm over the whole projection)
+        qn, kn = (config.q_size, config.kv_size) if config.qk_norm_full else (config.head_dim, config.head_dim)
+        self.q_norm = nn.Parameter(torch.ones(qn, **kw)) if config.qk_norm else None
+        self.k_norm = nn.Parameter(torch.ones(kn, **kw)) if config.qk_norm else None
         self.mlp_norm = nn.Parameter(torch.ones(h, **kw))
         if config.is_moe:
             e = config.num_experts
@@ -134,7 +136,17 @@ class CausalLM(nn.Module):
 
     # ---- forward -----------------------------------------------------------------------------------------------
     def embed_tokens(self, tokens: torch.Tensor) -> torch.Tensor:
-        return self.embed[tokens]
+        h = self.embed[tokens]
+        m = self.config.embedding_multiplier
+        return h if m == 1.0 else h * m
+
+    def _identity_rope(self, cos: torch.Tensor) -> tuple[torch.Tensor, torch.Tensor]:
+        """cos = 1, sin = 0 tables of ``cos``'s shape: rotary embedding that leaves q and k unchanged (NoPE)."""
+        cached = getattr(self, "_nope_tables", None)
+        if cached is None or cached[0].shape != cos.shape or cached[0].device != cos.device:
+            cached = (torch.ones_like(cos), torch.zeros_like(cos))
+            self._nope_tables = cached
+        return cached
 
     def forward_step(self, tokens: torch.Tensor, batch: StepBatch, cache: KVCache,
                      capture: tuple[int, ...] = (), layers: range | None = None, hidden: torch.Tensor | None = None,
@@ -150,6 +162,8 @@ class CausalLM(nn.Module):
             return sparse.chunked_forward(self, tokens, batch, cache, capture)
         if self._sequence_parallel(tokens, layers, hidden):
             return self._forward_sp(tokens, batch, cache, capture)
+        if c.post_norm:
+            return self._forward_post_norm(tokens, batch, cache, capture, layers, hidden)
         cos, sin = self.rope_tables()
         h = self.embed_tokens(tokens) if hidden is None else hidden
         resid: torch.Tensor | None = None
@@ -165,6 +179,7 @@ class CausalLM(nn.Module):
             x_in = None
             # a layer view may skip a sublayer (self-drafting): the pending branch output is added at the next norm
             if not getattr(layer, "skip_attn", False):
+                h, partial = self._scale_branch(h, partial)
                 x, resid = self._norm(h, layer.attn_norm, resid, partial)
                 if i in capture:
                     aux[i] = resid
@@ -174,6 +189,7 @@ class CausalLM(nn.Module):
             elif i in capture:
                 raise ValueError(f"cannot capture the input of layer {i}: its attention is skipped")
             if not getattr(layer, "skip_mlp", False):
+                h, partial = self._scale_branch(h, partial)
                 x, resid = self._norm(h, layer.mlp_norm, resid, partial)
                 h = self._mlp(layer, x, i)
                 partial = True
@@ -181,6 +197,7 @@ class CausalLM(nn.Module):
                 # dynamic depth: the policy decides, per token, how the layer's output enters the stream
                 out = resid + self._materialize(h, partial)
                 h, resid, partial = depth.combine(i, x_in, out, batch), None, False
+        h, partial = self._scale_branch(h, partial)
         out, resid = self._norm(h, self.norm, resid, partial)
         if c.num_layers in capture:
             aux[c.num_layers] = resid
@@ -188,6 +205,38 @@ class CausalLM(nn.Module):
             aux[-1] = out
         if -2 in capture:
             aux[-2] = resid
+        return out, aux
+
+    def _scale_branch(self, h, partial: bool):
+        """A branch output times Granite's residual multiplier before it joins the residual stream (a no-op for
+        the other families; the embeddings entering the first block are never scaled)."""
+        m = self.config.residual_multiplier
+        if m == 1.0 or not partial:
+            return h, partial
+        return self._materialize(h, partial) * m, False
+
+    def _forward_post_norm(self, tokens: torch.Tensor, batch: StepBatch, cache: KVCache, capture: tuple[int, ...],
+                           layers: range | None, hidden: torch.Tensor | None):
+        """:meth:`forward_step` for blocks whose norms follow the branches (OLMo-2):
+        ``h = h + norm(attn(h)); h = h + norm(mlp(h))``, then the final norm."""
+        c = self.config
+        eps = c.rms_norm_eps
+        cos, sin = self.rope_tables()
+        h = self.embed_tokens(tokens) if hidden is None else hidden
+        aux: dict[int, torch.Tensor] = {}
+        for i in (layers if layers is not None else range(c.num_layers)):
+            layer = self.layers[i]
+            if i in capture:
+                aux[i] = h
+            a = self._materialize(self._attention(layer, i, h, batch, cache, cos, sin), True)
+            h = h + ops.rmsnorm(a, layer.attn_norm, eps)[0]
+            m = self._materialize(self._mlp(layer, h, i), True)
+            h = h + ops.rmsnorm(m, layer.mlp_norm, eps)[0]
+        out = ops.rmsnorm(h, self.norm, eps)[0]
+        if c.num_layers in capture or -2 in capture:
+            aux[c.num_layers] = aux[-2] = h
+        if -1 in capture:
+            aux[-1] = out
         return out, aux
 
     # ---- sequence-parallel tensor parallelism ------------------------------------------------------------------
@@ -198,7 +247,9 @@ class CausalLM(nn.Module):
         sp = getattr(tp, "sp", None) if tp is not None else None
         if sp is None or layers is not None or hidden is not None or not sp.fits(tokens.numel()):
             return False
-        if self.config.is_moe or self.observer is not None or self.depth_policy is not None:
+        c = self.config
+        if c.is_moe or self.observer is not None or self.depth_policy is not None or c.post_norm or \
+                c.qk_norm_full or c.residual_multiplier != 1.0:
             return False
         return not any(getattr(layer, name, None) for layer in self.layers
                        for name in ("skip_attn", "skip_mlp", "mlp_rule", "attn_input_hook"))
@@ -291,9 +342,21 @@ class CausalLM(nn.Module):
         c = self.config
         k_cache, v_cache = cache.layer(index)
         k_scale, v_scale = cache.layer_scales(index)
+        q_norm, k_norm = layer.q_norm, layer.k_norm
+        if c.qk_norm_full and q_norm is not None:  # RMSNorm over all heads' features of q and of k (OLMo-2)
+            if isinstance(qkv, ops.Partials):
+                qkv = qkv.sum()
+            qs, ks = self.local["num_heads"] * c.head_dim, self.local["num_kv_heads"] * c.head_dim
+            q_part, k_part, v_part = qkv.split([qs, ks, ks], -1)
+            q_part = ops.rmsnorm(q_part.contiguous(), q_norm, c.rms_norm_eps)[0]
+            k_part = ops.rmsnorm(k_part.contiguous(), k_norm, c.rms_norm_eps)[0]
+            qkv = torch.cat([q_part, k_part, v_part], -1)
+            q_norm = k_norm = None
+        if index in c.nope_layers:
+            cos, sin = self._identity_rope(cos)
         q = ops.rope_store(qkv, batch.positions, cos, sin, self.local["num_heads"], self.local["num_kv_heads"],
                            c.head_dim, k_cache,
-                           v_cache, batch.kv_len, batch.n_new, layer.q_norm, layer.k_norm, c.rms_norm_eps,
+                           v_cache, batch.kv_len, batch.n_new, q_norm, k_norm, c.rms_norm_eps,
                            q_offset=batch.q_offset, k_scale=k_scale, v_scale=v_scale)
         keep = self.kv_evictor.keep_for(index, k_cache, q, batch) if self.kv_evictor is not None else None
         sparse = self.prefill_sparsity
@@ -304,8 +367,8 @@ class CausalLM(nn.Module):
         kivi = self.kv_quantizer.layer_args(index, cache) if self.kv_quantizer is not None else {}
         sparse_pass = sparse is not None and sparse.active
         tail = self.exact_tail if (not batch.prompt and q.shape[1] <= 64 and not sparse_pass) else 0
-        o = ops.attention(q, k_cache, v_cache, batch.kv_len, batch.n_new, batch.mask, q_offset=batch.q_offset,
-                          k_scale=k_scale, v_scale=v_scale, keep=keep, tail=tail, **kivi)
+        o = ops.attention(q, k_cache, v_cache, batch.kv_len, batch.n_new, batch.mask, scale=c.attention_multiplier,
+                          q_offset=batch.q_offset, k_scale=k_scale, v_scale=v_scale, keep=keep, tail=tail, **kivi)
         if self.kv_evictor is not None and batch.is_prefill:
             self.kv_evictor.observe_prefill(index, q, k_cache, v_cache, batch)
         return o.reshape(*o.shape[:2], -1)
@@ -332,7 +395,7 @@ class CausalLM(nn.Module):
             from ..parallel.moe import moe_mlp
 
             return moe_mlp(x, layer.router, layer.w_gate_up, layer.w_down, self.config.experts_per_token,
-                           getattr(self, "ep", None))
+                           getattr(self, "ep", None), renormalize=self.config.norm_topk_prob)
         if self.observer is not None:
             self.observer(index, "w_gate_up", x)
         rule = getattr(layer, "mlp_rule", None)  # activation-sparse MLPs (CATS, Deja Vu); None: the dense path
@@ -358,6 +421,9 @@ class CausalLM(nn.Module):
     def logits(self, hidden: torch.Tensor) -> torch.Tensor:
         """Logits over the full vocabulary (gathered from the vocabulary shards under tensor parallelism)."""
         local = ops.linear(hidden, self.head_weight)
+        scale = self.config.logits_scaling
+        if scale != 1.0:  # Granite divides its logits (a positive scale: the argmax is unchanged)
+            local = local / scale
         if self.tp is None or self.tp.size == 1:
             return local
         every = self.tp.all_gather(local)  # [P, ..., V/P]

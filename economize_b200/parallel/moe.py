@@ -39,12 +39,15 @@ def route(logits: torch.Tensor, k: int) -> tuple[torch.Tensor, torch.Tensor]:
 
 
 def moe_reference(x: torch.Tensor, router: torch.Tensor, w_gate_up: torch.Tensor, w_down: torch.Tensor,
-                  k: int, logits: torch.Tensor | None = None) -> torch.Tensor:
+                  k: int, renormalize: bool = True, logits: torch.Tensor | None = None) -> torch.Tensor:
     """The MoE MLP in plain PyTorch (fp32 accumulation of the weighted expert outputs); ``logits`` overrides the
     router output (to route exactly like another implementation)."""
     shape = x.shape
     x2 = x.reshape(-1, shape[-1])
-    ids, w = route(F.linear(x2, router) if logits is None else logits, k)
+    scores = F.linear(x2, router) if logits is None else logits
+    ids, w = route(scores, k)
+    if not renormalize:
+        w = w * torch.softmax(scores.float(), -1).gather(-1, ids).sum(-1, keepdim=True).to(w.dtype)
     out = torch.zeros(x2.shape[0], shape[-1], dtype=torch.float32, device=x.device)
     for e in range(w_gate_up.shape[0]):
         rows, slot = (ids == e).nonzero(as_tuple=True)
@@ -57,19 +60,26 @@ def moe_reference(x: torch.Tensor, router: torch.Tensor, w_gate_up: torch.Tensor
 
 
 def moe_mlp(x: torch.Tensor, router: torch.Tensor, w_gate_up: torch.Tensor, w_down: torch.Tensor,
-            k: int, ep: ExpertParallel | None = None) -> torch.Tensor:
-    """Top-``k`` MoE MLP of ``x [..., H]`` with experts ``w_gate_up [E, 2F, H]``, ``w_down [E, H, F]``."""
+            k: int, ep: ExpertParallel | None = None, renormalize: bool = True) -> torch.Tensor:
+    """Top-``k`` MoE MLP of ``x [..., H]`` with experts ``w_gate_up [E, 2F, H]``, ``w_down [E, H, F]``. The
+    chosen experts' softmax probabilities are renormalised to sum to one (Mixtral), or kept as they are
+    (``renormalize=False``, Qwen3-MoE's ``norm_topk_prob=False``)."""
     if ep is not None and ep.size > 1:
+        if not renormalize:
+            raise ConfigError("expert parallelism renormalises the top-k router weights")
         return ep.forward(x, router, w_gate_up, w_down, k)
     if not x.is_cuda:
-        return moe_reference(x, router, w_gate_up, w_down, k)
+        return moe_reference(x, router, w_gate_up, w_down, k, renormalize)
     from ..ops._ext import require
 
     C = require()
     shape = x.shape
     x2 = x.reshape(-1, shape[-1]).contiguous()
     logits = ops.linear(x2, router)
-    _, weights, pos, offsets = C.moe_route(logits, k)
+    ids, weights, pos, offsets = C.moe_route(logits, k)
+    if not renormalize:  # back from the renormalised weights to the softmax probabilities of the chosen experts
+        chosen = torch.softmax(logits.float(), -1).gather(-1, ids.long()).sum(-1, keepdim=True)
+        weights = weights * chosen
     xs = C.moe_gather(x2, pos)
     a = ops.silu_mul(C.linear_grouped(xs, w_gate_up, offsets))
     y = C.linear_grouped(a, w_down, offsets)

@@ -60,7 +60,11 @@ def layer_view(target: CausalLM, layers: Sequence[int | tuple[int, bool, bool]],
         if not 0 <= i < target.config.num_layers:
             raise ConfigError(f"layer {i} is outside the target's {target.config.num_layers} layers")
         refs.append(LayerRef(target.layers[i], sa, sm))
-    view.config = dataclasses.replace(target.config, num_layers=len(refs) + len(extra))
+    order = [spec if isinstance(spec, int) else spec[0] for spec in layers]
+    # per-layer attributes keyed by the target's layer index follow the layers into the view's numbering
+    view.config = dataclasses.replace(target.config, num_layers=len(refs) + len(extra),
+                                      nope_layers=tuple(j for j, i in enumerate(order)
+                                                        if i in target.config.nope_layers))
     view.embed = target.embed
     view.layers = nn.ModuleList(refs + list(extra))
     view.norm = target.norm
@@ -73,6 +77,7 @@ def layer_view(target: CausalLM, layers: Sequence[int | tuple[int, bool, bool]],
     view.kv_quantizer = None
     view.depth_policy = None
     view.prefill_sparsity = None
+    view.exact_tail = target.exact_tail
     if target.kv_scales is not None:
         idx = [spec if isinstance(spec, int) else spec[0] for spec in layers]
         ks, vs = target.kv_scales
