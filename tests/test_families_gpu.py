@@ -1,0 +1,46 @@
+"""The added model families on the CUDA path (bf16, sm_100a kernels): logits close to the fp32 CPU oracle of the
+same weights, and greedy tree decoding equal to plain decoding token for token."""
+
+import pytest
+import torch
+import transformers
+
+import economize_b200 as eco
+from economize_b200.models.llama import CausalLM
+from economize_b200.techniques.eagle3 import Eagle3Config
+
+pytestmark = pytest.mark.gpu
+
+BASE = dict(vocab_size=1024, hidden_size=512, intermediate_size=1024, num_hidden_layers=3, num_attention_heads=8,
+            num_key_value_heads=2, max_position_embeddings=1024, pad_token_id=0, rms_norm_eps=1e-6)
+FAMILIES = {
+    "granite": dict(embedding_multiplier=12.0, residual_multiplier=0.22, attention_multiplier=0.0078125,
+                    logits_scaling=8.0),
+    "phi3": dict(),
+    "smollm3": dict(no_rope_layers=[1, 0, 1]),
+    "olmo2": dict(),
+    "qwen3_moe": dict(num_experts=8, num_experts_per_tok=2, moe_intermediate_size=256, norm_topk_prob=False),
+}
+
+
+@pytest.mark.parametrize("name", list(FAMILIES))
+def test_family_on_gpu(cuda, name):
+    cfg = transformers.CONFIG_MAPPING[name](**{**BASE, **FAMILIES[name]})
+    torch.manual_seed(0)
+    hf = transformers.AutoModelForCausalLM.from_config(cfg).float().eval()
+    cpu = CausalLM.from_hf(hf)
+    gpu = CausalLM.from_hf(hf, dtype=torch.bfloat16, device=cuda)
+    ids = torch.randint(1, 1024, (1, 40), generator=torch.Generator().manual_seed(1))
+    want = eco.apply(cpu)(ids).float()
+    got = eco.apply(gpu)(ids.to(cuda)).float().cpu()
+    err = (got - want).abs().max().item()
+    assert err <= 0.05 * want.abs().max().item() + 0.02, err
+    em = eco.apply(gpu, Eagle3Config())
+    prompts = [ids[0].to(cuda), ids[0, :17].to(cuda)]
+    plain = em.decode_batch(prompts, 20, decoding=eco.DecodeConfig(cycle_length=1))
+    tree = em.decode_batch(prompts, 20, decoding=eco.DecodeConfig(
+        cycle_length=7, draft_policy="dynamic_tree", draft_policy_options={"depth": 6, "topk": 10, "total_tokens": 60},
+        cuda_graphs=True))
+    for a, b in zip(plain, tree):
+        assert torch.equal(a.tokens, b.tokens)
+    assert eco.ops.require().status(0) == 0
