@@ -171,7 +171,9 @@ __global__ void __launch_bounds__(256) rope_store_kernel(
     int S, int q_offset, const float* __restrict__ k_scale, const float* __restrict__ v_scale, Parts parts) {
   pdl_trigger();
   pdl_wait();
-  constexpr int E = D / 64;  // elements per lane in each half of the head (pairs of E / 2)
+  // each active lane owns E consecutive elements (whole bf16 pairs) of each half of the head: D = 64 uses 16 lanes
+  constexpr int E = D / 64 < 2 ? 2 : D / 64;
+  constexpr int kLanes = D / (2 * E);
   const int warp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
   const int lane = threadIdx.x & 31;
   const int slots = H + Hkv;
@@ -183,7 +185,8 @@ __global__ void __launch_bounds__(256) rope_store_kernel(
   const int width = (H + 2 * Hkv) * D;
   const size_t src = static_cast<size_t>(token) * width + (is_q ? head * D : H * D + (head - H) * D);
   // lane owns elements [E * lane, E * lane + E) of the first half and their partners in the second half
-  const int i0 = E * lane;
+  const bool active = lane < kLanes;
+  const int i0 = E * (active ? lane : 0);
   float x[E], y[E];
 #pragma unroll
   for (int e = 0; e < E; e += 2) {
@@ -197,13 +200,14 @@ __global__ void __launch_bounds__(256) rope_store_kernel(
     float part = 0.f;
 #pragma unroll
     for (int e = 0; e < E; ++e) part += x[e] * x[e] + y[e] * y[e];
-    const float inv = rsqrtf(warp_sum(part) / D + eps);
+    const float inv = rsqrtf(warp_sum(active ? part : 0.f) / D + eps);  // every lane joins the shuffle
 #pragma unroll
     for (int e = 0; e < E; ++e) {
       x[e] = bf16r(__bfloat162float(nw[i0 + e]) * bf16r(x[e] * inv));
       y[e] = bf16r(__bfloat162float(nw[i0 + e + D / 2]) * bf16r(y[e] * inv));
     }
   }
+  if (!active) return;
   const int pos = positions[token];
   const float* cp = cos_t + static_cast<size_t>(pos) * (D / 2) + i0;
   const float* sp = sin_t + static_cast<size_t>(pos) * (D / 2) + i0;
