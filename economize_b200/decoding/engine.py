@@ -52,6 +52,8 @@ class DecodeResult:
     tokens: torch.Tensor
     cycles: int = 0
     accepted: int = 0
+    #: every model call of the generation (:class:`~economize_b200.decoding.cost.CostLog`), when recorded
+    cost: object = None
 
     @property
     def mean_accepted(self) -> float:
@@ -98,6 +100,8 @@ class _State:
         self.max_new = torch.zeros(batch, **i32)
         self.accepted = torch.zeros(batch, dtype=torch.int64, device=dev)
         self.cycles = torch.zeros(batch, **i32)
+        # drafts accepted by each row's cycles, in order (column out_cap: a trash slot); read back for the cost log
+        self.acc_hist = torch.zeros(batch, out_cap + 1, **i32)
         # prompt + committed tokens + the pending root, slot p = position p (read by n-gram drafters)
         self.history = torch.zeros(batch, capacity + 1, dtype=torch.int64, device=dev)
         hidden = model.config.hidden_size
@@ -209,6 +213,7 @@ class SpecEngine:
         out = state.out[:, :out_cap].cpu()
         acc = state.accepted.cpu()
         cyc = state.cycles.cpu()
+        hist = state.acc_hist.cpu() if self.drafter is not None else None
         results = []
         for b in range(batch):
             toks = out[b, : min(int(n_out[b]), max_news[b])]
@@ -216,9 +221,65 @@ class SpecEngine:
                 hits = [i for i, t in enumerate(toks.tolist()) if t in stop_tokens]
                 if hits:
                     toks = toks[: hits[0] + 1]
-            results.append(DecodeResult(toks, int(cyc[b]), int(acc[b])))
+            accepted = hist[b, : int(cyc[b])].tolist() if hist is not None else [0] * int(cyc[b])
+            results.append(DecodeResult(toks, int(cyc[b]), int(acc[b]),
+                                        self.cost_log(int(lengths[b]), accepted)))
         self.stats.rows = results
         return results
+
+    # ---- cost accounting ---------------------------------------------------------------------------------------
+    def _draft_footprint(self):
+        from .cost import LayerFootprint
+
+        drafter = self.drafter
+        footprint = getattr(drafter, "footprint", None)
+        if footprint is not None:
+            return footprint() if callable(footprint) else footprint
+        name = getattr(drafter, "cost_module", None) or type(drafter).__name__.removesuffix("Drafter").lower()
+        return LayerFootprint.of(range(1, int(getattr(drafter, "num_layers", 1)) + 1), module=name)
+
+    def _draft_steps(self) -> list[int]:
+        """Tokens of each draft step of one cycle that runs a draft network (the first draft comes from the
+        previous cycle's observe pass, so a chain of k drafts makes k - 1 calls)."""
+        if self.drafter is None or self.static:
+            return []
+        if self.tree is not None:
+            return [self.tree.topk] * (self.tree.depth - 1)
+        if self.static_tree is not None:
+            return list(self._plan(self.model.device).widths[:-1]) if self.static_tree.depth > 1 else []
+        if self.search is not None:
+            return [self.search.width] * (self.search.depth - 1)
+        return [1] * (self.depth - 1)
+
+    def cost_log(self, prompt_tokens: int, accepted: list[int]):
+        """The model calls of one row: the prefill, then per cycle the draft steps, the verification pass over the
+        draft tree and the drafter's observe pass, with ``accepted[c]`` drafts accepted by cycle ``c``."""
+        from .cost import CostKind, CostLog, LayerFootprint
+
+        log = CostLog()
+        target = LayerFootprint.all(self.model.config.num_layers)
+        log.record_footprint(CostKind.EXACT, prompt_tokens, 0, target)
+        position = prompt_tokens
+        if self.drafter is None:
+            for _ in accepted:
+                log.record_footprint(CostKind.EXACT, 1, position, target)
+                position += 1
+            return log
+        draft = self._draft_footprint()
+        steps = self._draft_steps()
+        verified = 1 + (self.tree.total_tokens if self.tree is not None else
+                        self.static_tree.size if self.static_tree is not None else
+                        self.search.total_tokens if self.search is not None else
+                        self.drafter.draft_nodes(self.config) if self.static else self.depth)
+        observes = getattr(self.drafter, "observes", True) and not self.static
+        for n_acc in accepted:
+            for i, width in enumerate(steps):
+                log.record_footprint(CostKind.DRAFT, width, position + i + 1, draft, step=i + 1)
+            log.record_footprint(CostKind.EXACT, verified, position, target)
+            if observes:
+                log.record_footprint(CostKind.DRAFT_OBSERVE, n_acc + 2, position, draft)
+            position += n_acc + 1
+        return log
 
     # ---- state -------------------------------------------------------------------------------------------------
     def _state(self, batch: int, capacity: int, out_cap: int) -> _State:
@@ -356,8 +417,9 @@ class SpecEngine:
         pred = self._pred(hidden[:, 0])
         active = st.n_out < st.max_new
         st.out.scatter_(1, torch.where(active, st.n_out, st.out_cap).long()[:, None], pred[:, None])
-        st.n_out.add_(1)
-        st.kv_len.add_(1)
+        step = active.to(st.kv_len.dtype)
+        st.n_out.add_(step)  # finished rows keep their output length and their KV position
+        st.kv_len.add_(step)
         st.cycles.add_(active.int())
         st.last.copy_(pred)
 
@@ -402,6 +464,7 @@ class SpecEngine:
         keep = (col <= n_acc.long()[:, None]) & (idx < st.out_cap) & active[:, None]
         st.out.scatter_(1, torch.where(keep, idx, st.out_cap), out[:, :width])
         st.accepted.add_(torch.where(active, n_acc, 0).long())
+        st.acc_hist.scatter_(1, torch.where(active, st.cycles, st.out_cap).long()[:, None], n_acc[:, None].int())
         st.cycles.add_(active.int())
         hist_idx = st.kv_len.long()[:, None] + 1 + col
         hist_keep = (col <= n_acc.long()[:, None]) & (hist_idx < st.history.shape[1])

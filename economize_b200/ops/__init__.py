@@ -19,6 +19,7 @@ __all__ = [
     "argmax",
     "attention",
     "attention_scores",
+    "attention_usage",
     "available",
     "greedy_accept",
     "kivi_quantize",
@@ -134,12 +135,38 @@ def attention(q: torch.Tensor, k_cache: torch.Tensor, v_cache: torch.Tensor, kv_
     bit as a one-token pass at the same position does, for trees up to ``tail`` deep (the CPU path computes the
     same values without that rounding guarantee)."""
     scale = float(scale if scale is not None else q.shape[-1] ** -0.5)
+    _trace_attention(q, k_cache, mask, k_scale, keep, kivi, tail)
     if q.is_cuda:
         return require().attention(q, k_cache, v_cache, kv_len, n_new, mask, scale, int(q_offset), None, k_scale,
                                    v_scale, keep, lse_out, kivi, kivi_chunks, int(kivi_bits), int(tail))
     return reference.attention(q, k_cache, v_cache, kv_len, n_new, mask, scale, q_offset=q_offset, k_scale=k_scale,
                                v_scale=v_scale, keep=keep, lse_out=lse_out, kivi=kivi, kivi_chunks=kivi_chunks,
                                kivi_bits=kivi_bits)
+
+
+_ATTENTION_USAGE: dict[tuple[str, str, int, str], int] = {}
+
+
+def _trace_attention(q, k_cache, mask, k_scale, keep, kivi, tail) -> None:
+    device = "cuda" if q.is_cuda else "cpu"
+    cache = "kivi" if kivi is not None else "fp8" if k_scale is not None else str(k_cache.dtype).removeprefix("torch.")
+    parts = ["masked" if mask is not None else "causal"]
+    if tail:
+        parts.append("exact_tail")
+    if keep is not None:
+        parts.append("keep")
+    key = (device, cache, int(q.shape[1]), "+".join(parts))
+    _ATTENTION_USAGE[key] = _ATTENTION_USAGE.get(key, 0) + 1
+
+
+def attention_usage(reset: bool = False) -> dict[tuple[str, str, int, str], int]:
+    """Which attention paths ran: ``{(device, cache format, queries per row, mode): calls}``, counted when a call
+    is issued from Python (a captured CUDA graph counts its calls once, at capture). The tracing economize does in
+    ``attention/interface.py`` (``kernel_usage``)."""
+    usage = dict(_ATTENTION_USAGE)
+    if reset:
+        _ATTENTION_USAGE.clear()
+    return usage
 
 
 def kivi_quantize(cache: torch.Tensor, kivi: torch.Tensor, kv_len: torch.Tensor, chunks: torch.Tensor, bits: int,
