@@ -57,6 +57,11 @@ def parse() -> argparse.Namespace:
     p.add_argument("--nccl-tp", action="store_true", help="with tp: NCCL all-reduces instead of the fused kernels")
     p.add_argument("--attn", default=None, help="reference arm: attention implementation (default: economize's "
                    "own kernel, falling back to sdpa, then eager, if it cannot run)")
+    p.add_argument("--config", type=int, choices=(1, 2, 3, 4, 5), default=2,
+                   help="BASELINE.json configuration: 2 (default) is the headline; 1, 3, 4 and 5 run the "
+                   "compositions of economize_b200.bench.configs (this package's arm only)")
+    p.add_argument("--scale", choices=("full", "tiny"), default="full",
+                   help="configs 3-5: the named architecture, or a small one of the same composition")
     args = p.parse_args()
     if args.parallel is None:
         args.parallel = "tp" if int(os.environ.get("WORLD_SIZE", "1")) > 1 else "dp"
@@ -522,6 +527,49 @@ def run_ours(args, world, rank, log):
     return arm.model, step, results, prompts
 
 
+CONFIG_METRICS = {
+    1: "CPU fp32 plumbing: tiny Llama + EAGLE-3 chain of 4, tokens equal plain greedy",
+    3: "decode tok/s + mean accepted len, Llama-3.1-70B arch ShortGPT-8 int4 g128 fp8-KV int8-EAGLE-3, TP=8",
+    4: "decode tok/s + mean accepted len, Mixtral-8x7B-style MoE block-fp8 + Medusa-4, EP=8",
+    5: "decode tok/s + mean accepted len, 128K context KIVI-2 + StreamingLLM draft view + 1B draft on another GPU",
+}
+
+
+def run_config(args, world, rank, log):
+    """Configurations 1, 3, 4 and 5 (economize_b200.bench.configs) through this package's public API."""
+    from economize_b200.bench import configs
+
+    kw: dict = {}
+    if args.config != 1:
+        kw["scale"] = args.scale
+        kw["device"] = "cuda"
+    if args.config == 3 and world > 1:
+        from economize_b200.distributed import TPGroup
+
+        kw["tp"] = TPGroup(rank, world)
+    if args.config == 4 and world > 1:
+        from economize_b200.parallel.moe import FusedExpertParallel
+
+        kw["ep"] = FusedExpertParallel(rank, world, max_tokens=4096)
+    if args.config == 5 and torch.cuda.device_count() > 1:
+        kw["draft_device"] = f"cuda:{(torch.cuda.current_device() + 1) % torch.cuda.device_count()}"
+    if args.config == 1:
+        kw["device"] = "cuda"
+    spec = configs.build(args.config, **kw)
+    log(f"{spec.name}: {spec.notes}")
+    args.batch, args.new_tokens = len(spec.prompts), spec.new_tokens
+    args.prompt_len = int(spec.prompts[0].numel())
+    import economize_b200 as eco
+
+    results = {"cfg": spec.decoding, "streams": 1 if args.config == 3 else world,
+               "plain_cfg": eco.DecodeConfig(cycle_length=1), "spec": spec}
+
+    def step():
+        results["r"] = spec.step()
+
+    return spec.model, step, results, spec.prompts
+
+
 def acceptance(rows) -> tuple[int, int]:
     """(accepted drafts, verified cycles) over the rows of one step, for either implementation's results."""
     accepted = cycles = 0
@@ -566,7 +614,20 @@ def main() -> None:
         print(f"[bench r{rank}] {msg}", file=sys.stderr, flush=True)
 
     tp = args.parallel == "tp" and world > 1
-    if args.impl == "reference":
+    if args.config != 2 and args.impl == "reference":
+        if rank == 0:
+            print(json.dumps({"impl": "reference", "metric": CONFIG_METRICS[args.config],
+                              "unavailable": f"configuration {args.config} is a composition this bench drives "
+                              "through this package only; the reference publishes no number for it"}))
+        if world > 1:
+            import torch.distributed as dist
+
+            dist.destroy_process_group()
+        return
+    if args.config != 2:
+        model, step, results, prompts = run_config(args, world, rank, log)
+        tp = args.config in (3, 4) and world > 1
+    elif args.impl == "reference":
         built, why = run_reference(args, world, rank, log)
         ok = reduce_sum(0.0 if built is None else 1.0, world)
         if ok < world:  # every rank takes the same collective steps: all stop when one cannot run
@@ -634,8 +695,10 @@ def main() -> None:
     if rank == 0:
         parallelism = (f"tp{world}" + ("-nccl" if args.nccl_tp and args.impl == "ours" else
                                        "-fused" if args.impl == "ours" else "-hf-auto")) if tp else f"dp{world}"
+        if args.config == 4 and world > 1:
+            parallelism = f"ep{world}-fused"
         line = {
-            "metric": METRIC, "value": round(value, 2), "unit": "tok/s", "n_gpus": world, "steps": args.steps,
+            "metric": METRIC if args.config == 2 else CONFIG_METRICS[args.config], "value": round(value, 2), "unit": "tok/s", "n_gpus": world, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": round(ms_max, 3), "higher_is_better": True,
             "scaling": "strong" if tp else "weak",
             "vs_baseline": (value / BASELINE_TOKS) if BASELINE_TOKS else None, "dtype": "bf16",
@@ -658,6 +721,15 @@ def main() -> None:
         }
         if equal_plain is not None:
             line["tokens_equal_plain_greedy"] = equal_plain
+        if args.config != 2:
+            spec = results["spec"]
+            line["config"] = {"model": spec.name, "scale": args.scale if args.config != 1 else "fixed",
+                              "global_batch": args.batch * streams, "seq_len": args.prompt_len,
+                              "new_tokens": args.new_tokens, "parallelism": parallelism,
+                              "cuda_graphs": bool(getattr(spec.decoding, "cuda_graphs", False)),
+                              "l2": "weights exceed L2; no flush" if args.scale == "full" else
+                                    "small model: weights fit in L2 (not a roofline number)",
+                              **{k: v for k, v in spec.notes.items()}}
         if args.impl == "reference":
             line["impl"] = "reference"
             line["config"]["attn_implementation"] = results.get("attn")

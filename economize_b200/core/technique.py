@@ -48,6 +48,7 @@ class Family(enum.Enum):
 
     DRAFTER = "drafter"
     QUANTIZATION = "quantization"
+    DRAFT_COMPRESSION = "draft_compression"  # compresses the drafter's own weights (never the target's)
     PRUNING = "pruning"
     KV_COMPRESSION = "kv_compression"
     SPARSITY = "sparsity"

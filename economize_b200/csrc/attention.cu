@@ -25,6 +25,17 @@
 // bit as a one-token pass at the same position does (greedy speculative decoding reproduces plain decoding exactly)
 // as long as the tree is at most tail_w deep.
 //
+// Options (AttnOpts): tanh soft-capping of the scores (Gemma-2: s -> cap * tanh(s / cap), applied to the scaled
+// natural-log score), attention sinks (gpt-oss: one learned logit per query head that joins every row's softmax
+// denominator and contributes no value), and sliding windows (Mistral / Gemma-2/3 / OLMo-3 local layers: a query at
+// position p sees keys at positions > p - window). With a window the CTA walks only the chunks its rows can see,
+// and the key split is planned over the window's span with split boundaries at absolute multiples of the chunks per
+// split, so passes of different widths still reduce a row's keys in the same groups.
+//
+// Head dimension 256 (Gemma): Q [128, 256] and one stage each of K and V [128, 256] fill the shared memory (the row
+// partials share the P tile), so K of the next chunk streams while P . V runs and V while the next S runs; the
+// accumulator uses TMEM columns [128, 384) of a 512-column allocation.
+//
 // fp8 caches (e4m3 codes with one static scale per KV head, K = s_k * K8, V = s_v * V8): TMA brings the raw
 // [128 keys, 128 B] code tiles into a double-buffered staging ring, all threads convert them to bf16 (exact: every
 // e4m3 value is a bf16 value) in the swizzled layout the UMMAs read, and the scales are applied outside the tensor
@@ -48,7 +59,11 @@ constexpr int kAtom = kRows * 128;          // bytes of one 64-column swizzled h
 constexpr int kTile = 2 * kAtom;            // a 128 x 128 bf16 tile
 constexpr int kSmem = 6 * kTile + 1024 + 64 + 4 * 128 * 4;  // Q, P, 2 x K, 2 x V, barriers, row partials
 // the same layout for head dimension D (Q [128, D], P [128, 128], two stages of K and V [128, D])
-__host__ __device__ constexpr int attn_smem_bytes(int D) { return kRows * D * 2 + kTile + 4 * kKeys * D * 2 + 1024 + 64 + 4 * 128 * 4; }
+__host__ __device__ constexpr int attn_smem_bytes(int D) {
+  return D == 256 ? kRows * D * 2 + kTile + 2 * kKeys * D * 2 + 1024 + 64  // one K/V stage; partials in the P tile
+                  : kRows * D * 2 + kTile + 4 * kKeys * D * 2 + 1024 + 64 + 4 * 128 * 4;
+}
+static_assert(attn_smem_bytes(256) <= 232448, "the D = 256 layout must fit 227 KB");
 static_assert(attn_smem_bytes(128) == kSmem, "the D = 128 layout is the reference footprint");
 constexpr int kRawTile = kKeys * kDim;                        // one fp8 code tile (128 keys x 128 B)
 // fp8: Q, P, converted K, converted V, then 2 stages x (raw K, raw V): the same 6 x kTile
@@ -164,6 +179,12 @@ __device__ __forceinline__ uint32_t visible32(int s0, int base, int nn, bool use
   return vis;
 }
 
+// Bits i of the 32 slots [s0, s0 + 32) with s0 + i >= lo (the sliding window's first visible slot).
+__device__ __forceinline__ uint32_t at_or_above(int s0, int lo) {
+  const long k = static_cast<long>(lo) - s0;
+  return k <= 0 ? 0xffffffffu : (k >= 32 ? 0u : ~((1u << k) - 1u));
+}
+
 __device__ __forceinline__ float fast_exp2(float x) {
   float y;
   asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
@@ -175,7 +196,8 @@ __device__ __forceinline__ float fast_exp2(float x) {
 template <int D>
 __device__ __forceinline__ void merge_row(const float* __restrict__ ws_o, const float* __restrict__ ws_ml,
                                           bf16* __restrict__ out, int tile, int r, int lane, int T, int H, int Hkv,
-                                          int m_tiles, int splits, float* __restrict__ lse_out) {
+                                          int m_tiles, int splits, float* __restrict__ lse_out,
+                                          const float* __restrict__ sinks) {
   const int m_tile = tile % m_tiles, bh = tile / m_tiles;
   const int b = bh / Hkv, kvh = bh % Hkv;
   const int G = H / Hkv;
@@ -188,6 +210,8 @@ __device__ __forceinline__ void merge_row(const float* __restrict__ ws_o, const 
     const size_t slot = (static_cast<size_t>(tile) * splits + s) * kRows + r;
     if (ws_ml[slot * 2 + 1] > 0.f) mx = fmaxf(mx, ws_ml[slot * 2]);
   }
+  const float sink2 = sinks != nullptr ? sinks[head] * 1.4426950408889634f : -INFINITY;
+  mx = fmaxf(mx, sink2);  // a sink logit joins the denominator only
   constexpr int E = D / 32;
   float acc[E];
 #pragma unroll
@@ -203,6 +227,7 @@ __device__ __forceinline__ void merge_row(const float* __restrict__ ws_o, const 
     for (int e = 0; e < E; ++e) acc[e] += v[e] * w;
     denom += l * w;
   }
+  if (sinks != nullptr) denom += exp2f(sink2 - mx);
   const float inv = denom > 0.f ? 1.f / denom : 0.f;
   if (lse_out != nullptr && lane == 0)
     lse_out[(static_cast<size_t>(b) * T + t) * H + head] = denom > 0.f ? mx + __log2f(denom) : -INFINITY;
@@ -225,27 +250,33 @@ __global__ void __launch_bounds__(kThreads, 1)
                    int chunks_per_split, int m_tiles, unsigned* status, unsigned long long* trace,
                    const float* __restrict__ k_scale, const float* __restrict__ v_scale,
                    const uint32_t* __restrict__ keep, float* __restrict__ lse_out,
-                   const uint8_t* __restrict__ kivi, const int* __restrict__ kivi_chunks, int kivi_bits, int tail_w) {
+                   const uint8_t* __restrict__ kivi, const int* __restrict__ kivi_chunks, int kivi_bits, int tail_w,
+                   AttnOpts opts) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  static_assert(D == 64 || D == 128, "head dimensions 64 and 128");
+  static_assert(D == 64 || D == 128 || D == 256, "head dimensions 64, 128 and 256");
   static_assert(!FP8 || D == 128, "fp8 caches at head dimension 128");
+  constexpr bool kSingle = D == 256;       // one K/V stage (see the file comment)
   constexpr int kQTile = kRows * D * 2;    // Q [128 rows, D]
   constexpr int kKVTile = kKeys * D * 2;   // one K or V chunk [128 keys, D]
   constexpr int kDQ = D / 4;               // output columns per quarter of the CTA
   constexpr int kAtoms = D / 64;           // 64-column swizzled atoms per row
+  constexpr int kStages = kSingle ? 1 : 2;
+  constexpr uint32_t kTmemCols = kSingle ? 512 : 256;
   uint8_t* q_tile = smem;
   uint8_t* p_tile = smem + kQTile;
-  // bf16: two stages of K and V tiles; fp8: one converted K and V tile, then two stages of raw codes
+  // bf16: kStages stages of K and V tiles; fp8: one converted K and V tile, then two stages of raw codes
   uint8_t* k_tiles = p_tile + kTile;
-  uint8_t* v_tiles = FP8 ? k_tiles + kTile : k_tiles + 2 * kKVTile;
+  uint8_t* v_tiles = FP8 ? k_tiles + kTile : k_tiles + kStages * kKVTile;
   uint8_t* raw = smem + 4 * kTile;  // fp8 stage s: raw K at s * 2 * kRawTile, raw V after it
-  uint64_t* kv_full = reinterpret_cast<uint64_t*>(p_tile + kTile + 4 * kKVTile);
+  // kv_full[s]: stage s of K and V (kSingle: [0] = K, [1] = V)
+  uint64_t* kv_full = reinterpret_cast<uint64_t*>(p_tile + kTile + 2 * kStages * kKVTile);
   uint64_t* bar_s = kv_full + 2;
   uint64_t* bar_pv = bar_s + 1;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bar_pv + 1);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
-  float* red = reinterpret_cast<float*>(reinterpret_cast<uint8_t*>(kv_full) + 64);  // [4][128] row partials
+  // [4][128] row partials (kSingle: inside the P tile, free whenever the partials are in use)
+  float* red = kSingle ? reinterpret_cast<float*>(p_tile) : reinterpret_cast<float*>(reinterpret_cast<uint8_t*>(kv_full) + 64);
 
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int quad = warp & 3, quarter = warp >> 2;
@@ -259,7 +290,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   const int m_tile = blockIdx.x % m_tiles;
   const int bh = blockIdx.x / m_tiles;
   const int b = bh / Hkv, kvh = bh % Hkv;
-  const int split = blockIdx.y, splits = gridDim.y;
+  const int split = blockIdx.y;
   const int G = H / Hkv;
 
   const int p = m_tile * kRows + r;
@@ -271,19 +302,26 @@ __global__ void __launch_bounds__(kThreads, 1)
   const bool use_mask = mask != nullptr;
   const uint64_t bits = (row_valid && use_mask) ? static_cast<uint64_t>(mask[static_cast<size_t>(b) * T + t]) : 0ull;
   const int causal_lim = q_offset + t + 1;
+  // the query's position minus the committed length (tree depth, or its index among the new tokens)
+  const int qdepth = use_mask ? max(0, __popcll(bits) - 1) : (q_offset + t);
+  const int wlo = (opts.window > 0 && row_valid) ? base + qdepth - opts.window + 1 : INT_MIN;  // first visible slot
 
   const int t_last = min(T - 1, ((m_tile + 1) * kRows - 1) / G);
   const bool tail = tail_w > 0;
   // exact-tail mode: this row's tensor-core keys are the committed slots below its position minus tail_w
   int tc_lim = 0;
-  if (tail && row_valid) {
-    const int depth = max(0, use_mask ? (__popcll(bits) - 1) : (q_offset + t));
-    tc_lim = max(0, min(base, base + depth - tail_w));
-  }
+  if (tail && row_valid) tc_lim = max(0, min(base, base + qdepth - tail_w));
   int visible_end = tail ? base : use_mask ? base + nn : base + min(nn, q_offset + t_last + 1);
   visible_end = min(visible_end, S);
   const int n_chunks = (visible_end + kKeys - 1) / kKeys;
-  const int c0 = split * chunks_per_split;
+  // with a window, split groups start at the group of the first chunk any row of the tile can see
+  int g0 = 0;
+  if (opts.window > 0) {
+    const int t_first = min(T - 1, (m_tile * kRows) / G);
+    const int pos_min = base + (use_mask ? 0 : q_offset + t_first);
+    g0 = (max(0, pos_min - opts.window + 1) / kKeys) / chunks_per_split;
+  }
+  const int c0 = (g0 + split) * chunks_per_split;
   const int c1 = min(n_chunks, c0 + chunks_per_split);
 
   const size_t kv_row0 = (static_cast<size_t>(b) * Hkv + kvh) * S;
@@ -307,6 +345,15 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
     }
   };
+  // kSingle: K and V of chunk c into the single stage, each on its own barrier
+  auto issue_one = [&](int c, bool is_v) {
+    const int y = static_cast<int>(kv_row0 + static_cast<size_t>(c) * kKeys);
+    uint64_t* bar = &kv_full[is_v ? 1 : 0];
+    uint8_t* dst = is_v ? v_tiles : k_tiles;
+    mbar_arrive_expect_tx(bar, kAtoms * kAtom);
+#pragma unroll
+    for (int a = 0; a < kAtoms; ++a) tma_load_2d(dst + a * kAtom, is_v ? &tm_v : &tm_k, bar, 64 * a, y);
+  };
   // Chunks whose committed keys are all hidden by the keep bitmap (and that hold no new key) are skipped: the
   // CTA walks the active chunks only, every thread computing the same sequence from the bitmap.
   auto active = [&](int c) -> bool {
@@ -319,6 +366,10 @@ __global__ void __launch_bounds__(kThreads, 1)
     return c;
   };
   if constexpr (FP8) scale_log2 *= k_scale[kvh];  // S = s_k * (Q . K8^T)
+  // soft-cap: s2 = cap log2(e) tanh(raw * scale / cap) (scale_log2 = scale log2(e))
+  const bool capped = opts.softcap > 0.f;
+  const float cap_in = capped ? scale_log2 / (1.4426950408889634f * opts.softcap) : 0.f;
+  const float cap_out = capped ? opts.softcap * 1.4426950408889634f : 0.f;
   if (tid == 0) {
     mbar_init(&kv_full[0], 1);
     mbar_init(&kv_full[1], 1);
@@ -326,14 +377,21 @@ __global__ void __launch_bounds__(kThreads, 1)
     mbar_init(bar_pv, 1);
     *abort_flag = 0;
     fence_mbar_init();
-    // the first two active K/V chunks stream while the CTA allocates TMEM and stages Q
+    // the first active K/V chunks stream while the CTA allocates TMEM and stages Q
     const int a0 = next_active(c0);
-    const int a1 = a0 < c1 ? next_active(a0 + 1) : c1;
-    if (a0 < c1) issue_kv(a0, 0);
-    if (a1 < c1) issue_kv(a1, 1);
+    if constexpr (kSingle) {
+      if (a0 < c1) {
+        issue_one(a0, false);
+        issue_one(a0, true);
+      }
+    } else {
+      const int a1 = a0 < c1 ? next_active(a0 + 1) : c1;
+      if (a0 < c1) issue_kv(a0, 0);
+      if (a1 < c1) issue_kv(a1, 1);
+    }
   }
   __syncwarp();
-  if (warp == 0) tmem_alloc(tmem_slot, 256);
+  if (warp == 0) tmem_alloc(tmem_slot, kTmemCols);
 
   // Q row r, 16-byte chunks [quarter * D / 32, + D / 32) -> swizzled K-major tile (zeros for padding rows)
   {
@@ -368,8 +426,8 @@ __global__ void __launch_bounds__(kThreads, 1)
   int c_next = c < c1 ? next_active(c + 1) : c1;
   for (int i = 0; c < c1 && ok; ++i) {
     const int c_after = c_next < c1 ? next_active(c_next + 1) : c1;  // the chunk two ahead (prefetched below)
-    const int s = i & 1;
-    const uint32_t kv_phase = (i >> 1) & 1;
+    const int s = kSingle ? 0 : (i & 1);
+    const uint32_t kv_phase = kSingle ? (i & 1) : ((i >> 1) & 1);
     const uint32_t ph = i & 1;
     ok = mbar_wait(&kv_full[s], kv_phase, status, kStatusWaitFull, abort_flag);
     if (!ok) break;
@@ -379,7 +437,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       fence_async_smem();
       tc_fence_before();
       __syncthreads();
-    } else {
+    } else if constexpr (!kSingle) {
       if (c < q_chunks) {  // stage s was last read by chunk c - 2, whose MMAs have completed
         const size_t chunk_id = (static_cast<size_t>(b) * Hkv + kvh) * (S / kKeys) + c;
         dequant_kivi_tile(kivi + chunk_id * kivi_chunk_bytes(kivi_bits), kivi_bits, k_tiles + s * kKVTile,
@@ -408,30 +466,40 @@ __global__ void __launch_bounds__(kThreads, 1)
     if (!ok) break;
     __syncwarp();
     tc_fence_after();
+    if constexpr (kSingle) {  // the S MMA has read K: the next chunk's K streams during this chunk's softmax and PV
+      if (tid == 0 && c_next < c1) issue_one(c_next, false);
+    }
     if (stamp && i == 0) stamp[3] = global_timer_ns();
 
     // this thread's 32 scores of the chunk
     float sc[32];
     tmem_ld16(tmem_s + lane_off, sc);
     tmem_ld16(tmem_s + lane_off + 16, sc + 16);
-    uint32_t vis = tail ? visible32(c * kKeys + col0, tc_lim, 0, false, 0ull, 0, row_valid)
-                        : visible32(c * kKeys + col0, base, nn, use_mask, bits, causal_lim, row_valid);
+    const int s0 = c * kKeys + col0;
+    uint32_t vis = tail ? visible32(s0, tc_lim, 0, false, 0ull, 0, row_valid)
+                        : visible32(s0, base, nn, use_mask, bits, causal_lim, row_valid);
     if (keep != nullptr) {  // evicted committed slots are invisible (new slots are never evicted)
-      const int s0 = c * kKeys + col0;
       const uint32_t kw = keep[(static_cast<size_t>(b) * Hkv + kvh) * (S / 32) + s0 / 32];
       const int pre = min(max(base - s0, 0), 32);
       const uint32_t committed = pre >= 32 ? 0xffffffffu : ((1u << pre) - 1u);
       vis &= kw | ~committed;
     }
+    if (opts.window > 0) vis &= at_or_above(s0, wlo);
     float qmax = -INFINITY;
+    if (capped) {
 #pragma unroll
-    for (int j = 0; j < 32; ++j) {
-      sc[j] *= scale_log2;
-      if ((vis >> j) & 1u) qmax = fmaxf(qmax, sc[j]);
+      for (int j = 0; j < 32; ++j) sc[j] = cap_out * tanhf(sc[j] * cap_in);
+    } else {
+#pragma unroll
+      for (int j = 0; j < 32; ++j) sc[j] *= scale_log2;
     }
+#pragma unroll
+    for (int j = 0; j < 32; ++j)
+      if ((vis >> j) & 1u) qmax = fmaxf(qmax, sc[j]);
     red[quarter * kRows + r] = qmax;
     __syncthreads();
     const float cmax = fmaxf(fmaxf(red[r], red[kRows + r]), fmaxf(red[2 * kRows + r], red[3 * kRows + r]));
+    if constexpr (kSingle) __syncthreads();  // every thread has read the partials before P overwrites them
     const float m_new = fmaxf(m_run, cmax);
     const float alpha = m_new == -INFINITY ? 1.f : fast_exp2(m_run - m_new);
     float csum = 0.f;
@@ -458,6 +526,10 @@ __global__ void __launch_bounds__(kThreads, 1)
     if constexpr (FP8) {  // every thread has converted stage s: its raw codes may be overwritten
       if (tid == 0 && c_after < c1) issue_kv(c_after, s);
     }
+    if constexpr (kSingle) {
+      ok = mbar_wait(&kv_full[1], ph, status, kStatusWaitFull, abort_flag);
+      if (!ok) break;
+    }
     if (tid == 0) {
       tc_fence_after();
       const uint32_t pa = smem_u32(p_tile), va = smem_u32(v_tiles + (FP8 ? 0 : s * kKVTile));
@@ -475,13 +547,19 @@ __global__ void __launch_bounds__(kThreads, 1)
     __syncwarp();
     tc_fence_after();
     if (stamp && i == 0) stamp[5] = global_timer_ns();
-    if (!FP8 && tid == 0 && c_after < c1) issue_kv(c_after, s);  // both MMAs reading stage s are done
+    if constexpr (kSingle) {  // the PV MMA has read V: the next chunk's V streams during its S and softmax
+      if (tid == 0 && c_next < c1) issue_one(c_next, true);
+    } else if constexpr (!FP8) {
+      if (tid == 0 && c_after < c1) issue_kv(c_after, s);  // both MMAs reading stage s are done
+    }
     __syncwarp();
-    float pv[kDQ];
 #pragma unroll
-    for (int c16 = 0; c16 < kDQ; c16 += 16) tmem_ld16(tmem_pv + lane_off + c16, pv + c16);
+    for (int c16 = 0; c16 < kDQ; c16 += 16) {  // 16 columns at a time keeps D = 256 within the register budget
+      float pv[16];
+      tmem_ld16(tmem_pv + lane_off + c16, pv);
 #pragma unroll
-    for (int d = 0; d < kDQ; ++d) o[d] = o[d] * alpha + pv[d];
+      for (int d = 0; d < 16; ++d) o[c16 + d] = o[c16 + d] * alpha + pv[d];
+    }
     c = c_next;
     c_next = c_after;
   }
@@ -500,10 +578,18 @@ __global__ void __launch_bounds__(kThreads, 1)
   }
 
   if (!failed && row_valid) {
-    if (splits == 1 && !tail) {
+    if (gridDim.y == 1 && !tail) {
+      // a sink logit joins the denominator: rescale to the larger of the row maximum and the sink
+      float m_fin = m_run, l_fin = l_tot, fac = 1.f;
+      if (opts.sinks != nullptr) {
+        const float s2 = opts.sinks[head] * 1.4426950408889634f;
+        m_fin = fmaxf(m_run, s2);
+        fac = exp2f(m_run - m_fin);
+        l_fin = l_tot * fac + exp2f(s2 - m_fin);
+      }
       if (lse_out != nullptr && quarter == 0)  // log2-domain log-sum-exp of the row's scaled scores
-        lse_out[(static_cast<size_t>(b) * T + t) * H + head] = l_tot > 0.f ? m_run + __log2f(l_tot) : -INFINITY;
-      const float inv = l_tot > 0.f ? 1.f / l_tot : 0.f;
+        lse_out[(static_cast<size_t>(b) * T + t) * H + head] = l_fin > 0.f ? m_fin + __log2f(l_fin) : -INFINITY;
+      const float inv = l_fin > 0.f ? fac / l_fin : 0.f;
       uint4* dst = reinterpret_cast<uint4*>(out + ((static_cast<size_t>(b) * T + t) * H + head) * D + ocol0);
 #pragma unroll
       for (int c = 0; c < kDQ / 8; ++c) {
@@ -516,7 +602,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         dst[c] = make_uint4(w[0], w[1], w[2], w[3]);
       }
     } else {
-      const size_t slot = (static_cast<size_t>(blockIdx.x) * splits + split) * kRows + r;
+      const size_t slot = (static_cast<size_t>(blockIdx.x) * gridDim.y + split) * kRows + r;
       float4* dst = reinterpret_cast<float4*>(ws_o + slot * D + ocol0);
 #pragma unroll
       for (int c = 0; c < kDQ / 4; ++c) dst[c] = make_float4(o[4 * c], o[4 * c + 1], o[4 * c + 2], o[4 * c + 3]);
@@ -526,7 +612,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
     }
   }
-  if (warp == 0) tmem_dealloc(tmem, 256);
+  if (warp == 0) tmem_dealloc(tmem, kTmemCols);
   if (stamp) stamp[7] = global_timer_ns();
 }
 
@@ -536,11 +622,12 @@ template <int D>
 __global__ void __launch_bounds__(128) attn_merge_kernel(const float* __restrict__ ws_o,
                                                          const float* __restrict__ ws_ml, bf16* __restrict__ out,
                                                          int T, int H, int Hkv, int m_tiles, int splits,
-                                                         float* __restrict__ lse_out) {
+                                                         float* __restrict__ lse_out,
+                                                         const float* __restrict__ sinks) {
   pdl_trigger();
   pdl_wait();
   merge_row<D>(ws_o, ws_ml, out, blockIdx.x, blockIdx.y * 4 + (threadIdx.x >> 5), threadIdx.x & 31, T, H, Hkv, m_tiles,
-            splits, lse_out);
+            splits, lse_out, sinks);
 }
 
 // Exact-tail merge: one warp per packed row combines the tensor-core partials of every split with the row's tail
@@ -567,11 +654,13 @@ __device__ __forceinline__ void load_kv(const uint8_t* base, size_t row, int lan
 }
 
 template <int E>
-__device__ __forceinline__ float tail_score(const float* qv, const float* kv, float scale_log2) {
+__device__ __forceinline__ float tail_score(const float* qv, const float* kv, float scale_log2, float cap_in,
+                                           float cap_out) {
   float d = qv[0] * kv[0];
 #pragma unroll
   for (int e = 1; e < E; ++e) d = fmaf(qv[e], kv[e], d);
-  return warp_sum(d) * scale_log2;
+  const float raw = warp_sum(d);
+  return cap_out > 0.f ? cap_out * tanhf(raw * cap_in) : raw * scale_log2;
 }
 
 constexpr int kTailKeysMax = 128;  // committed tail (tail_w <= 64) + new keys (at most 64)
@@ -584,7 +673,7 @@ __global__ void __launch_bounds__(128) attn_merge_tail_kernel(
     const uint8_t* __restrict__ k_cache, const uint8_t* __restrict__ v_cache, const int* __restrict__ kv_len,
     const int* __restrict__ n_new, const int64_t* __restrict__ mask, int S, float scale_log2, int q_offset,
     int tail_w, const float* __restrict__ k_scale, const float* __restrict__ v_scale,
-    const uint32_t* __restrict__ keep) {
+    const uint32_t* __restrict__ keep, float softcap, const float* __restrict__ sinks) {
   __shared__ int s_row[4][kTailKeysMax];    // cache rows of this warp's tail keys, in position order
   __shared__ float s_sc[4][kTailKeysMax];   // their scaled scores
   pdl_trigger();
@@ -601,6 +690,8 @@ __global__ void __launch_bounds__(128) attn_merge_tail_kernel(
   const bool fp8 = k_scale != nullptr;
   const float sl = fp8 ? scale_log2 * k_scale[kvh] : scale_log2;
   const float sv = fp8 ? v_scale[kvh] : 1.f;
+  const float cap_in = softcap > 0.f ? sl / (1.4426950408889634f * softcap) : 0.f;
+  const float cap_out = softcap > 0.f ? softcap * 1.4426950408889634f : 0.f;
   const int base = kv_len[b], nn = n_new[b];
   const bool use_mask = mask != nullptr;
   const uint64_t bits = use_mask ? static_cast<uint64_t>(mask[static_cast<size_t>(b) * T + t]) : 0ull;
@@ -639,6 +730,8 @@ __global__ void __launch_bounds__(128) attn_merge_tail_kernel(
     const size_t slot = (static_cast<size_t>(tile) * splits + sp) * kRows + r;
     if (ws_ml[slot * 2 + 1] > 0.f) mx = fmaxf(mx, ws_ml[slot * 2]);
   }
+  const float sink2 = sinks != nullptr ? sinks[head] * 1.4426950408889634f : -INFINITY;
+  mx = fmaxf(mx, sink2);
   for (int i0 = 0; i0 < n_keys; i0 += kTailBatch) {
     float kv[kTailBatch][E];
 #pragma unroll
@@ -647,7 +740,7 @@ __global__ void __launch_bounds__(128) attn_merge_tail_kernel(
 #pragma unroll
     for (int u = 0; u < kTailBatch; ++u) {
       if (i0 + u < n_keys) {
-        const float sc = tail_score<E>(qv, kv[u], sl);
+        const float sc = tail_score<E>(qv, kv[u], sl, cap_in, cap_out);
         if (lane == 0) s_sc[wid][i0 + u] = sc;
         mx = fmaxf(mx, sc);
       }
@@ -685,6 +778,7 @@ __global__ void __launch_bounds__(128) attn_merge_tail_kernel(
       }
     }
   }
+  if (sinks != nullptr) denom += exp2f(sink2 - mx);
 
   const float inv = denom > 0.f ? 1.f / denom : 0.f;
   if (lse_out != nullptr && lane == 0)
@@ -893,16 +987,22 @@ __global__ void kivi_advance_kernel(const int* __restrict__ kv_len, int* __restr
 
 // The split over keys depends on the batch, the KV heads and the cache size only (not on the number of query
 // tokens), so a one-token pass and a verification pass reduce a row's keys in the same order.
-AttnPlan attention_plan(int B, int T, int H, int Hkv, int S, int num_sms, bool tail, int D) {
+// With a sliding window the split covers the window's span (the chunks one tile's rows can see: the window, up to
+// 128 positions of rows, and one chunk of misalignment) plus one group, because the CTAs start at the absolute
+// group of their first visible chunk.
+AttnPlan attention_plan(int B, int T, int H, int Hkv, int S, int num_sms, bool tail, int D, int window) {
   AttnPlan plan;
   const int G = H / Hkv;
   plan.m_tiles = (T * G + kRows - 1) / kRows;
   const int total_chunks = (S + kKeys - 1) / kKeys;
+  const int span = window > 0 ? std::min(total_chunks, (window + 2 * kKeys - 1) / kKeys + 1) : total_chunks;
   const int heads = B * Hkv;
   int splits = 1;
-  if (heads < num_sms) splits = std::min(total_chunks, std::max(1, (2 * num_sms) / heads));
-  plan.chunks_per_split = (total_chunks + splits - 1) / splits;
-  plan.splits = (total_chunks + plan.chunks_per_split - 1) / plan.chunks_per_split;
+  if (heads < num_sms) splits = std::min(span, std::max(1, (2 * num_sms) / heads));
+  plan.chunks_per_split = (span + splits - 1) / splits;
+  plan.splits = (span + plan.chunks_per_split - 1) / plan.chunks_per_split;
+  if (span < total_chunks)
+    plan.splits = std::min(plan.splits + 1, (total_chunks + plan.chunks_per_split - 1) / plan.chunks_per_split);
   const long ctas = static_cast<long>(heads) * plan.m_tiles;
   plan.ws_floats = (plan.splits > 1 || tail) ? ctas * plan.splits * kRows * (D + 2) : 0;
   plan.tail = tail;
@@ -914,11 +1014,15 @@ int launch_attention(const void* q, const CUtensorMap* tm_k, const CUtensorMap* 
                      int S, float scale, int q_offset, const AttnPlan& plan, unsigned* status, cudaStream_t stream,
                      unsigned long long* trace, const float* k_scale, const float* v_scale, const uint32_t* keep,
                      float* lse_out, const uint8_t* kivi, const int* kivi_chunks, int kivi_bits, int tail_w,
-                     const void* k_cache, const void* v_cache) {
+                     const void* k_cache, const void* v_cache, const AttnOpts& opts) {
   if (kivi != nullptr && (k_scale != nullptr || (kivi_bits != 2 && kivi_bits != 4))) return -1;
   if (tail_w < 0 || tail_w > 64 || (tail_w > 0 && (!plan.tail || k_cache == nullptr || v_cache == nullptr)))
     return -1;
-  if ((D != 64 && D != 128) || H % Hkv != 0) return -1;
+  if ((D != 64 && D != 128 && D != 256) || H % Hkv != 0) return -1;
+  if (opts.softcap < 0.f || opts.window < 0) return -1;
+  // a window must cover a tree (up to 64 new keys) and the exact tail: those keys are never filtered
+  if (opts.window > 0 && ((mask != nullptr && opts.window <= 64) || (tail_w > 0 && opts.window <= tail_w)))
+    return -2;
   if (mask != nullptr && T > 64) return -1;
   const bool fp8 = k_scale != nullptr;
   if (fp8 && v_scale == nullptr) return -1;
@@ -934,24 +1038,26 @@ int launch_attention(const void* q, const CUtensorMap* tm_k, const CUtensorMap* 
     launch_pdl(kernel, grid, dim3(kThreads), smem, stream, static_cast<const bf16*>(q), *tm_k, *tm_v,
                static_cast<bf16*>(out), ws_o, ws_ml, kv_len, n_new, mask, T, H, Hkv, S, sl2, q_offset,
                plan.chunks_per_split, plan.m_tiles, status, trace, k_scale, v_scale, keep, lse_out, kivi, kivi_chunks,
-               kivi_bits, tail_w);
+               kivi_bits, tail_w, opts);
   };
   if (D == 64) run(attn_tc_kernel<false, 64>, attn_smem_bytes(64));
+  else if (D == 256) run(attn_tc_kernel<false, 256>, attn_smem_bytes(256));
   else if (fp8) run(attn_tc_kernel<true, 128>, kSmem);
   else run(attn_tc_kernel<false, 128>, kSmem);
   dim3 mgrid(ctas, kRows / 4);
   if (tail_w > 0) {
-    auto merge = D == 64 ? attn_merge_tail_kernel<64> : attn_merge_tail_kernel<128>;
+    auto merge = D == 64 ? attn_merge_tail_kernel<64> : D == 256 ? attn_merge_tail_kernel<256>
+                                                                 : attn_merge_tail_kernel<128>;
     launch_pdl(merge, mgrid, dim3(128), 0, stream, static_cast<const float*>(ws_o),
                static_cast<const float*>(ws_ml), static_cast<bf16*>(out), T, H, Hkv, plan.m_tiles, plan.splits,
                lse_out, static_cast<const bf16*>(q), static_cast<const uint8_t*>(k_cache),
                static_cast<const uint8_t*>(v_cache), kv_len, n_new, mask, S, sl2, q_offset, tail_w, k_scale, v_scale,
-               keep);
+               keep, opts.softcap, opts.sinks);
   } else if (plan.splits > 1) {
-    auto merge = D == 64 ? attn_merge_kernel<64> : attn_merge_kernel<128>;
+    auto merge = D == 64 ? attn_merge_kernel<64> : D == 256 ? attn_merge_kernel<256> : attn_merge_kernel<128>;
     launch_pdl(merge, mgrid, dim3(128), 0, stream, static_cast<const float*>(ws_o),
                static_cast<const float*>(ws_ml), static_cast<bf16*>(out), T, H, Hkv, plan.m_tiles, plan.splits,
-               lse_out);
+               lse_out, opts.sinks);
   }
   return 0;
 }

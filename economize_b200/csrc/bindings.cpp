@@ -224,11 +224,23 @@ Tensor rope_store(Tensor qkv, Tensor positions, Tensor cos, Tensor sin, int64_t 
 Tensor attention(Tensor q, Tensor k_cache, Tensor v_cache, Tensor kv_len, Tensor n_new, c10::optional<Tensor> mask,
                  double scale, int64_t q_offset, c10::optional<Tensor> trace, c10::optional<Tensor> k_scale,
                  c10::optional<Tensor> v_scale, c10::optional<Tensor> keep, c10::optional<Tensor> lse_out,
-                 c10::optional<Tensor> kivi, c10::optional<Tensor> kivi_chunks, int64_t kivi_bits, int64_t tail) {
+                 c10::optional<Tensor> kivi, c10::optional<Tensor> kivi_chunks, int64_t kivi_bits, int64_t tail,
+                 double softcap, c10::optional<Tensor> sinks, int64_t window) {
   CHECK_CUDA(q);
   CHECK_BF16(q);
-  TORCH_CHECK(q.dim() == 4 && (q.size(3) == 128 || q.size(3) == 64) && k_cache.dim() == 4,
-              "attention: head_dim must be 64 or 128");
+  TORCH_CHECK(q.dim() == 4 && (q.size(3) == 128 || q.size(3) == 64 || q.size(3) == 256) && k_cache.dim() == 4,
+              "attention: head_dim must be 64, 128 or 256");
+  TORCH_CHECK(softcap >= 0.0 && window >= 0, "attention: softcap and window must be >= 0");
+  if (sinks.has_value()) {
+    CHECK_ON(*sinks, q);
+    TORCH_CHECK(sinks->scalar_type() == at::kFloat && sinks->is_contiguous() && sinks->numel() == q.size(2),
+                "attention: sinks must be fp32 [H] (one logit per query head)");
+  }
+  if (window > 0) {
+    TORCH_CHECK(!mask.has_value() || window > 64, "attention: a sliding window must exceed 64 positions in tree "
+                "passes");
+    TORCH_CHECK(tail == 0 || window > tail, "attention: a sliding window must exceed the exact tail");
+  }
   TORCH_CHECK(tail >= 0 && tail <= 64, "attention: the exact tail covers 0 .. 64 positions");
   const bool fp8 = fp8_cache(k_cache, k_scale, v_scale, k_cache.size(1));
   TORCH_CHECK(v_cache.scalar_type() == k_cache.scalar_type(), "K and V caches must share a dtype");
@@ -278,7 +290,12 @@ Tensor attention(Tensor q, Tensor k_cache, Tensor v_cache, Tensor kv_len, Tensor
   auto out = at::empty_like(q);
   if (tail > 0) TORCH_CHECK(T <= 64, "attention: the exact tail serves passes of at most 64 query tokens");
   TORCH_CHECK(k_cache.size(3) == D && v_cache.size(3) == D, "attention: caches must have q's head_dim");
-  const ecz::AttnPlan plan = ecz::attention_plan(B, T, H, Hkv, S, num_sms(q.get_device()), tail > 0, D);
+  const ecz::AttnPlan plan = ecz::attention_plan(B, T, H, Hkv, S, num_sms(q.get_device()), tail > 0, D,
+                                                 static_cast<int>(window));
+  ecz::AttnOpts opts;
+  opts.softcap = static_cast<float>(softcap);
+  opts.sinks = sinks.has_value() ? sinks->data_ptr<float>() : nullptr;
+  opts.window = static_cast<int>(window);
   Tensor ws;
   if (plan.ws_floats > 0) ws = at::empty({plan.ws_floats}, q.options().dtype(at::kFloat));
   const uint64_t rows = static_cast<uint64_t>(B) * Hkv * S;
@@ -303,13 +320,13 @@ Tensor attention(Tensor q, Tensor k_cache, Tensor v_cache, Tensor kv_len, Tensor
                                        kivi.has_value() ? kivi->data_ptr<uint8_t>() : nullptr,
                                        kivi.has_value() ? kivi_chunks->data_ptr<int>() : nullptr,
                                        static_cast<int>(kivi_bits), static_cast<int>(tail), k_cache.data_ptr(),
-                                       v_cache.data_ptr());
-  TORCH_CHECK(rc == 0, "attention: unsupported shape (head_dim 64 or 128, fp8 and KIVI caches at 128, H divisible "
-              "by H_kv)");
+                                       v_cache.data_ptr(), opts);
+  TORCH_CHECK(rc == 0, "attention: unsupported shape (head_dim 64, 128 or 256, fp8 and KIVI caches at 128, H "
+              "divisible by H_kv)");
   return out;
 }
 
-Tensor silu_mul(Tensor gu) {
+Tensor glu_act(Tensor gu, int64_t act) {
   CHECK_CUDA(gu);
   c10::cuda::CUDAGuard guard(gu.device());
   gu = gu.contiguous();
@@ -320,12 +337,14 @@ Tensor silu_mul(Tensor gu) {
   const int rows = static_cast<int>(numel / F2);
   shape.back() = F2 / 2;
   auto out = at::empty(shape, gu.options().dtype(at::kBFloat16));
-  const int rc = ecz::launch_silu_mul(splits ? nullptr : gu.data_ptr(), out.data_ptr(), rows, F2 / 2,
-                                      at::cuda::getCurrentCUDAStream(), splits ? gu.data_ptr<float>() : nullptr,
-                                      splits);
-  TORCH_CHECK(rc == 0, "silu_mul: width must be a multiple of 16");
+  const int rc = ecz::launch_glu(splits ? nullptr : gu.data_ptr(), out.data_ptr(), rows, F2 / 2,
+                                 at::cuda::getCurrentCUDAStream(), splits ? gu.data_ptr<float>() : nullptr, splits,
+                                 static_cast<int>(act));
+  TORCH_CHECK(rc == 0, "glu: width must be a multiple of 16 and act 0 (SiLU) or 1 (GELU tanh)");
   return out;
 }
+
+Tensor silu_mul(Tensor gu) { return glu_act(gu, 0); }
 
 Tensor linear_bf16(Tensor x, Tensor w) {
   CHECK_CUDA(x);
@@ -1300,8 +1319,8 @@ int64_t ep_wait_probe(int64_t ptr, int64_t experts_local, int64_t cap, int64_t h
 }
 
 std::tuple<int64_t, int64_t, int64_t> attention_plan(int64_t B, int64_t T, int64_t H, int64_t Hkv, int64_t S,
-                                                     int64_t sms) {
-  const ecz::AttnPlan p = ecz::attention_plan(B, T, H, Hkv, S, sms);
+                                                     int64_t sms, int64_t window) {
+  const ecz::AttnPlan p = ecz::attention_plan(B, T, H, Hkv, S, sms, false, 128, static_cast<int>(window));
   return {p.m_tiles, p.splits, p.chunks_per_split};
 }
 
@@ -1328,11 +1347,12 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
         py::arg("scale"), py::arg("q_offset"), py::arg("trace") = py::none(), py::arg("k_scale") = py::none(),
         py::arg("v_scale") = py::none(), py::arg("keep") = py::none(), py::arg("lse_out") = py::none(),
         py::arg("kivi") = py::none(), py::arg("kivi_chunks") = py::none(), py::arg("kivi_bits") = 0,
-        py::arg("tail") = 0);
+        py::arg("tail") = 0, py::arg("softcap") = 0.0, py::arg("sinks") = py::none(), py::arg("window") = 0);
   m.def("kivi_chunk_size", &ecz::kivi_chunk_size, "bytes of one KIVI-coded 128-key chunk");
   m.def("kivi_quantize", &kivi_quantize, "quantise committed cache chunks to KIVI codes and advance the counts");
   m.def("attention_scores", &attention_scores, "accumulate KV-eviction attention scores (tcgen05)");
   m.def("silu_mul", &silu_mul, "SwiGLU activation of [gate; up]");
+  m.def("glu", &glu_act, "act(gate) * up of [gate; up]: act 0 = SiLU, 1 = GELU (tanh approximation)");
   m.def("linear_parts", &linear_parts, "x @ w.T as bf16 or fp32 split-K partials for a fusing consumer");
   m.def("moe_route", &moe_route, "top-k expert routing with deterministic expert-order positions");
   m.def("moe_gather", &moe_gather, "permute token rows into expert order");
@@ -1384,7 +1404,8 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("sp_linear_rs", &sp_linear_rs, "GEMM -> reduce-scatter (rows stored into their owner's partial slot)");
   m.def("reduce_rmsnorm", &reduce_rmsnorm, "wait for every rank's partial, sum, add residual, RMSNorm");
   m.def("status", &status, "read and clear the device status word of bounded waits");
-  m.def("attention_plan", &attention_plan, "(m_tiles, splits, chunks_per_split) of an attention launch");
+  m.def("attention_plan", &attention_plan, "(m_tiles, splits, chunks_per_split) of an attention launch",
+        py::arg("B"), py::arg("T"), py::arg("H"), py::arg("Hkv"), py::arg("S"), py::arg("sms"), py::arg("window") = 0);
   m.def("gemm_splits", &gemm_splits, "split-K factor of a GEMM launch");
   m.def("gemm_cluster_splits", &gemm_cluster_splits, "cluster size of the cluster split-K GEMM");
 }

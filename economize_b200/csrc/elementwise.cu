@@ -2,7 +2,7 @@
 //   * rmsnorm_kernel      fused residual add + RMSNorm (one CTA per token row, 16-byte vector loads)
 //   * rope_store_kernel   optional per-head RMSNorm (QK-norm families) + rotary embedding of q and k, and the
 //                         KV-cache write of k and v (one warp per token x head)
-//   * silu_mul_kernel     SwiGLU activation of a fused [gate; up] projection
+//   * glu_kernel          SwiGLU / GeGLU activation of a fused [gate; up] projection
 //   * argmax_kernel       first index of the row maximum (one CTA per row)
 //   * greedy_accept_kernel longest accepted path of a verified draft tree (one warp per row)
 //   * kv_compact_kernel   moves the accepted path's K/V to consecutive slots in all layers at once
@@ -281,10 +281,21 @@ int launch_rope_store(const void* qkv, const int* positions, const float* cos_t,
 }
 
 // ---------------------------------------------------------------------------------------------------------------
-// SiLU(gate) * up
+// act(gate) * up: SiLU (SwiGLU) or the tanh approximation of GELU (GeGLU, Gemma's gelu_pytorch_tanh)
 // ---------------------------------------------------------------------------------------------------------------
-__global__ void __launch_bounds__(256) silu_mul_kernel(const bf16* __restrict__ gu, bf16* __restrict__ out,
-                                                       int rows, int F, Parts parts) {
+template <int kAct>
+__device__ __forceinline__ float glu_act(float x) {
+  if constexpr (kAct == 0) {
+    return x / (1.f + expf(-x));
+  } else {  // 0.5 x (1 + tanh(sqrt(2 / pi) (x + 0.044715 x^3)))
+    const float inner = 0.7978845608028654f * fmaf(0.044715f * x, x * x, x);
+    return 0.5f * x * (1.f + tanhf(inner));
+  }
+}
+
+template <int kAct>
+__global__ void __launch_bounds__(256) glu_kernel(const bf16* __restrict__ gu, bf16* __restrict__ out, int rows,
+                                                  int F, Parts parts) {
   pdl_trigger();
   pdl_wait();
   const long total = static_cast<long>(rows) * (F / 8);
@@ -299,24 +310,28 @@ __global__ void __launch_bounds__(256) silu_mul_kernel(const bf16* __restrict__ 
     bf16* op = reinterpret_cast<bf16*>(&o);
 #pragma unroll
     for (int j = 0; j < 8; ++j) {
-      const float x = __bfloat162float(gp[j]);
-      const float s = bf16r(x / (1.f + expf(-x)));
+      const float s = bf16r(glu_act<kAct>(__bfloat162float(gp[j])));
       op[j] = __float2bfloat16(s * __bfloat162float(up[j]));
     }
     reinterpret_cast<uint4*>(out + r * F)[c] = o;
   }
 }
 
-int launch_silu_mul(const void* gu, void* out, int rows, int F, cudaStream_t stream, const float* gu_parts,
-                    int splits) {
-  if (F % 8 != 0) return -1;
+int launch_glu(const void* gu, void* out, int rows, int F, cudaStream_t stream, const float* gu_parts, int splits,
+               int act) {
+  if (F % 8 != 0 || act < 0 || act > 1) return -1;
   const Parts parts{gu_parts, splits, static_cast<long>(rows) * 2 * F};
   const long total = static_cast<long>(rows) * (F / 8);
   int blocks = static_cast<int>(std::min<long>((total + 255) / 256, 148L * 16));
   if (blocks < 1) blocks = 1;
-  launch_pdl(silu_mul_kernel, dim3(blocks), dim3(256), 0, stream, static_cast<const bf16*>(gu),
-             static_cast<bf16*>(out), rows, F, parts);
+  launch_pdl(act == 0 ? glu_kernel<0> : glu_kernel<1>, dim3(blocks), dim3(256), 0, stream,
+             static_cast<const bf16*>(gu), static_cast<bf16*>(out), rows, F, parts);
   return 0;
+}
+
+int launch_silu_mul(const void* gu, void* out, int rows, int F, cudaStream_t stream, const float* gu_parts,
+                    int splits) {
+  return launch_glu(gu, out, rows, F, stream, gu_parts, splits, 0);
 }
 
 // ---------------------------------------------------------------------------------------------------------------
@@ -478,38 +493,58 @@ int launch_greedy_accept(const int64_t* tokens, const int64_t* parents, const in
 // One CTA per (layer*2 + kv, b, kv head); every thread reads its 16-byte chunk first, then all write, so
 // overlapping source/destination slots of one path never race.
 // ---------------------------------------------------------------------------------------------------------------
+// Every (path position, 16-byte vector) pair of a row is read into registers before any is written (a source slot
+// may be another position's destination); a thread owns up to kCompactPer pairs, so rows of up to 64 vectors (D = 256
+// bf16) move 64 path positions deep in one 1024-thread block.
+constexpr int kCompactPer = 4;
+
 __global__ void kv_compact_kernel(uint8_t* __restrict__ cache, const int* __restrict__ kv_len,
                                   const int* __restrict__ path, const int* __restrict__ n_acc, int B, int Hkv, int S,
-                                  int row_bytes, int T) {
+                                  int row_bytes, int T, int max_depth) {
   pdl_trigger();
   pdl_wait();
   const int lh = blockIdx.x;  // layer*2 + kv
   const int b = blockIdx.y, h = blockIdx.z;
   const int n = n_acc[b];
   const int vecs = row_bytes / 16;
-  const int i = threadIdx.x / vecs + 1;  // path position (the root at 0 never moves)
-  const int c = threadIdx.x % vecs;
+  const int pairs = max_depth * vecs;
   uint8_t* base = cache + ((static_cast<size_t>(lh) * B + b) * Hkv + h) * static_cast<size_t>(S) * row_bytes;
   const int start = kv_len[b];
-  uint4 v = make_uint4(0, 0, 0, 0);
-  const bool active = i <= n && i < T;
-  int src = 0;
-  if (active) {
-    src = path[static_cast<size_t>(b) * T + i];
-    v = reinterpret_cast<const uint4*>(base + static_cast<size_t>(start + src) * row_bytes)[c];
+  uint4 v[kCompactPer];
+  int dst[kCompactPer];
+#pragma unroll
+  for (int u = 0; u < kCompactPer; ++u) {
+    const int pr = threadIdx.x + u * blockDim.x;
+    const int i = pr / vecs + 1;  // path position (the root at 0 never moves)
+    dst[u] = -1;
+    if (pr < pairs && i <= n && i < T) {
+      const int src = path[static_cast<size_t>(b) * T + i];
+      if (src != i) {
+        v[u] = reinterpret_cast<const uint4*>(base + static_cast<size_t>(start + src) * row_bytes)[pr % vecs];
+        dst[u] = i;
+      }
+    }
   }
   __syncthreads();
-  if (active && src != i) reinterpret_cast<uint4*>(base + static_cast<size_t>(start + i) * row_bytes)[c] = v;
+#pragma unroll
+  for (int u = 0; u < kCompactPer; ++u) {
+    if (dst[u] >= 0) {
+      const int pr = threadIdx.x + u * blockDim.x;
+      reinterpret_cast<uint4*>(base + static_cast<size_t>(start + dst[u]) * row_bytes)[pr % vecs] = v[u];
+    }
+  }
 }
 
 // Rows of `row_bytes` bytes (D * element size: bf16 and fp8 caches alike).
 int launch_kv_compact(void* cache, const int* kv_len, const int* path, const int* n_acc, int LH, int B, int Hkv,
                       int S, int row_bytes, int T, int max_depth, cudaStream_t stream) {
-  const int threads = max_depth * (row_bytes / 16);
-  if (threads > 1024 || row_bytes % 16) return -1;
+  if (row_bytes % 16 || max_depth < 1) return -1;
+  const int pairs = max_depth * (row_bytes / 16);
+  const int threads = std::min(1024, ((pairs + 31) / 32) * 32);
+  if (pairs > threads * kCompactPer) return -1;
   dim3 grid(LH, B, Hkv);
   launch_pdl(kv_compact_kernel, grid, dim3(threads), 0, stream, static_cast<uint8_t*>(cache), kv_len, path, n_acc,
-             B, Hkv, S, row_bytes, T);
+             B, Hkv, S, row_bytes, T, max_depth);
   return 0;
 }
 

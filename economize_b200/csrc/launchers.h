@@ -49,6 +49,14 @@ struct AgWait {
   int world = 0;
 };
 
+// Score options of an attention launch: tanh soft-cap of the scaled scores (0: off), one sink logit per query head
+// (fp32 [H], natural-log units; nullptr: off), sliding window in positions (0: off).
+struct AttnOpts {
+  float softcap = 0.f;
+  const float* sinks = nullptr;
+  int window = 0;
+};
+
 struct AttnPlan {
   int m_tiles = 1;
   int splits = 1;
@@ -67,6 +75,9 @@ int launch_rope_store(const void* qkv, const int* positions, const float* cos_t,
                       const void* k_norm, float eps, int B, int T, int H, int Hkv, int D, int S, int q_offset,
                       cudaStream_t stream, const float* k_scale = nullptr, const float* v_scale = nullptr,
                       const float* qkv_parts = nullptr, int splits = 0);
+// act(gate) * up of a fused [gate; up] projection: act 0 = SiLU, 1 = GELU (tanh approximation)
+int launch_glu(const void* gu, void* out, int rows, int F, cudaStream_t stream, const float* gu_parts, int splits,
+               int act);
 int launch_silu_mul(const void* gu, void* out, int rows, int F, cudaStream_t stream, const float* gu_parts = nullptr,
                     int splits = 0);
 int argmax_slices(int rows, int V);
@@ -102,14 +113,16 @@ int launch_gemm_persistent(const CUtensorMap* tm_w, const CUtensorMap* tm_x, voi
                            int N, int K, int num_sms, unsigned* status, cudaStream_t stream);
 
 // attention.cu
-AttnPlan attention_plan(int B, int T, int H, int Hkv, int S, int num_sms, bool tail = false, int D = 128);
+AttnPlan attention_plan(int B, int T, int H, int Hkv, int S, int num_sms, bool tail = false, int D = 128,
+                        int window = 0);
 int launch_attention(const void* q, const CUtensorMap* tm_k, const CUtensorMap* tm_v, void* out, float* ws,
                      const int* kv_len, const int* n_new, const int64_t* mask, int B, int T, int H, int Hkv, int D,
                      int S, float scale, int q_offset, const AttnPlan& plan, unsigned* status, cudaStream_t stream,
                      unsigned long long* trace = nullptr, const float* k_scale = nullptr,
                      const float* v_scale = nullptr, const uint32_t* keep = nullptr, float* lse_out = nullptr,
                      const uint8_t* kivi = nullptr, const int* kivi_chunks = nullptr, int kivi_bits = 0,
-                     int tail_w = 0, const void* k_cache = nullptr, const void* v_cache = nullptr);
+                     int tail_w = 0, const void* k_cache = nullptr, const void* v_cache = nullptr,
+                     const AttnOpts& opts = AttnOpts());
 // KIVI: bytes of one quantized 128-key chunk; quantise committed chunks of a bf16 cache [L, 2, B, Hkv, S, D] into
 // kivi [L, B, Hkv, S / 128, chunk bytes] and advance chunks [B] (at most max_new chunks per row and call)
 int kivi_chunk_size(int bits);

@@ -18,6 +18,7 @@ finish any row yet, so no cycle waits on the host.
 
 from __future__ import annotations
 
+import functools
 import math
 from dataclasses import dataclass, field
 
@@ -30,6 +31,7 @@ from ..runtime.cache import KVCache, StepBatch
 from ..runtime.phase import phase
 from .config import DecodeConfig
 from .drafter import DraftModel
+from .kv_stats import held_bytes, keep_snapshot, row_kv_stats
 from .policies import POLICIES, ConfidencePolicy, DynamicTreePolicy, SequoiaPolicy, SpecExecPolicy
 from .sequoia import AcceptanceProfile, StaticPlan, StaticTree, record_cycle
 from .specexec import SearchOptions
@@ -54,6 +56,17 @@ class DecodeResult:
     accepted: int = 0
     #: every model call of the generation (:class:`~economize_b200.decoding.cost.CostLog`), when recorded
     cost: object = None
+    #: computes the row's KV memory accounting on first access (see :attr:`kv`)
+    _kv_source: object = field(default=None, repr=False, compare=False)
+    _kv: object = field(default=None, repr=False, compare=False)
+
+    @property
+    def kv(self):
+        """KV-cache bytes of the row (:class:`~economize_b200.decoding.kv_stats.RowKVStats`: stored and full-format
+        committed bytes at the last pass, and the bytes attention read summed over the passes)."""
+        if self._kv is None and self._kv_source is not None:
+            self._kv = self._kv_source()
+        return self._kv
 
     @property
     def mean_accepted(self) -> float:
@@ -75,6 +88,8 @@ class GenerationStats:
     cycles: int = 0
     graph_replays: int = 0
     host_syncs: int = 0
+    #: measured bytes of the last generation's KV buffers (cache, KIVI codes, keep bitmaps)
+    kv_allocated_bytes: int = 0
     rows: list[DecodeResult] = field(default_factory=list)
 
     @property
@@ -215,6 +230,7 @@ class SpecEngine:
         cyc = state.cycles.cpu()
         hist = state.acc_hist.cpu() if self.drafter is not None else None
         results = []
+        keep = keep_snapshot(self.model)
         for b in range(batch):
             toks = out[b, : min(int(n_out[b]), max_news[b])]
             if stop_tokens:
@@ -222,9 +238,11 @@ class SpecEngine:
                 if hits:
                     toks = toks[: hits[0] + 1]
             accepted = hist[b, : int(cyc[b])].tolist() if hist is not None else [0] * int(cyc[b])
-            results.append(DecodeResult(toks, int(cyc[b]), int(acc[b]),
-                                        self.cost_log(int(lengths[b]), accepted)))
+            res = DecodeResult(toks, int(cyc[b]), int(acc[b]), self.cost_log(int(lengths[b]), accepted))
+            res._kv_source = functools.partial(row_kv_stats, self.model, keep, b, int(lengths[b]), accepted)
+            results.append(res)
         self.stats.rows = results
+        self.stats.kv_allocated_bytes = held_bytes(self.model, state.cache)
         return results
 
     # ---- cost accounting ---------------------------------------------------------------------------------------
@@ -452,7 +470,11 @@ class SpecEngine:
         sb = StepBatch(st.kv_len, n_new, positions, bits)
         with phase("refresh"):
             hidden, aux = model.forward_step(tokens.clamp_min(0), sb, st.cache, drafter.capture_layers)
+        self.last_pred = None
         n_acc, path, out = self._verify(tokens, parents, hidden, draft_tokens, q_full)
+        after = getattr(drafter, "after_verify", None)
+        if after is not None:  # host-side drafters that read the pass's predictions at their own nodes
+            after(tokens, self.last_pred)
         if self.acceptance is not None:  # Sequoia rate measurement: one host synchronization per cycle
             record_cycle(self.acceptance, self.static_tree, self._plan(dev), tokens, path, n_acc, out)
         ops.kv_compact(st.cache.data, st.kv_len, path, n_acc)
@@ -581,6 +603,7 @@ class SpecEngine:
             path = torch.minimum(path, n_acc[:, None]).contiguous()
             return n_acc, path, out
         pred = self.model.greedy(hidden) if plain_greedy else self._choose(logits)  # [B, T]
+        self.last_pred = pred  # read by drafters that learn from the target's predictions (lookahead's window)
         if self.accept_all:
             pred = torch.cat([drafts.clamp_min(0), pred[:, -1:]], 1)
             return ops.greedy_accept(tokens, parents, pred)

@@ -23,8 +23,17 @@ __all__ = ["ModelConfig", "SUPPORTED_MODEL_TYPES", "llama31_8b", "llama31_70b", 
 #: (mixtral, qwen3_moe), embedding / residual / attention / logit multipliers (granite), fused projections in the
 #: checkpoint (phi3), layers without rotary embedding (smollm3), norms after each branch and q/k RMSNorm over all
 #: heads (olmo2).
+#: Also: GeGLU MLPs, (1 + w) RMSNorms and a dtype-rounded embedding scale (gemma, gemma2, gemma3_text), a norm
+#: before and after each branch with tanh soft-capped attention scores and logits (gemma2) or per-head q/k norms and
+#: separate rotary tables for the sliding-window layers (gemma3_text), per-layer sliding windows (mistral, ministral,
+#: gemma2, gemma3_text, olmo3, qwen2 with use_sliding_window), sparse MoE with q/k norms (olmoe) and a gated shared
+#: expert (qwen2_moe).
 SUPPORTED_MODEL_TYPES = ("llama", "mistral", "qwen2", "qwen3", "mixtral", "granite", "phi3", "smollm3", "olmo2",
-                         "qwen3_moe", "economize_b200")
+                         "qwen3_moe", "gemma", "gemma2", "gemma3_text", "ministral", "olmo3", "olmoe", "qwen2_moe",
+                         "economize_b200")
+
+#: the layer kinds of ``ModelConfig.layer_types``
+FULL, SLIDING = "full_attention", "sliding_attention"
 
 
 @dataclass
@@ -60,14 +69,49 @@ class ModelConfig:
     qk_norm_full: bool = False
     #: layers whose attention runs without rotary embedding (SmolLM3's NoPE layers)
     nope_layers: tuple[int, ...] = ()
+    #: gated MLP activation: "silu" (SwiGLU) or "gelu_tanh" (GeGLU, Gemma)
+    hidden_act: str = "silu"
+    #: Gemma's RMSNorms scale by (1 + w): checkpoints store w, this model stores 1 + w
+    norm_unit_offset: bool = False
+    #: the embedding multiplier is rounded to the model dtype before it multiplies (Gemma's normalizer)
+    embedding_multiplier_in_dtype: bool = False
+    #: Gemma-2/3 blocks: an RMSNorm before and after each branch (OLMo-2's post_norm has only the one after)
+    sandwich_norm: bool = False
+    #: tanh soft-caps (s -> cap * tanh(s / cap)) of the attention scores and of the final logits (Gemma-2)
+    attn_softcap: float | None = None
+    final_softcap: float | None = None
+    #: attention kind of every layer ("full_attention" / "sliding_attention"; empty: all full) and the window
+    layer_types: tuple[str, ...] = ()
+    sliding_window: int = 0
+    #: rotary parameters of the sliding-window layers when they differ from the others' (Gemma-3: {"rope_theta":
+    #: 1e4}; keys as ``rope_scaling`` plus ``rope_theta``)
+    local_rope: dict[str, Any] | None = None
+    #: width of a shared expert added to every sparse MoE MLP, gated by sigmoid(x . w) (Qwen2-MoE; 0: none)
+    shared_expert_size: int = 0
     extra: dict[str, Any] = field(default_factory=dict)
 
     def __post_init__(self) -> None:
         if self.head_dim is None:
             self.head_dim = self.hidden_size // self.num_heads
         self.nope_layers = tuple(int(i) for i in self.nope_layers)
+        self.layer_types = tuple(str(t) for t in self.layer_types)
         if self.num_heads % self.num_kv_heads:
             raise UnsupportedModelError(f"{self.num_heads} heads do not split into {self.num_kv_heads} KV groups")
+        if self.hidden_act not in ("silu", "gelu_tanh"):
+            raise UnsupportedModelError(f"gated activation {self.hidden_act!r} is not supported")
+        if self.layer_types and len(self.layer_types) != self.num_layers:
+            raise UnsupportedModelError(f"{len(self.layer_types)} layer types for {self.num_layers} layers")
+        unknown = set(self.layer_types) - {FULL, SLIDING}
+        if unknown:
+            raise UnsupportedModelError(f"layer types {sorted(unknown)} are not supported")
+        if SLIDING in self.layer_types and self.sliding_window < 1:
+            raise UnsupportedModelError("sliding-window layers need sliding_window >= 1")
+
+    def window_of(self, layer: int) -> int:
+        """The attention window of ``layer`` in positions (0: the whole context)."""
+        if self.layer_types and self.layer_types[layer] == SLIDING:
+            return int(self.sliding_window)
+        return 0
 
     @property
     def q_size(self) -> int:
@@ -85,6 +129,7 @@ class ModelConfig:
         h, f, layers = self.hidden_size, self.intermediate_size, self.num_layers
         attn = h * (self.q_size + 2 * self.kv_size) + self.q_size * h
         mlp = 3 * h * f * (self.num_experts if self.is_moe else 1) + (h * self.num_experts if self.is_moe else 0)
+        mlp += 3 * h * self.shared_expert_size + (h if self.shared_expert_size else 0)
         embed = self.vocab_size * h * (1 if self.tie_word_embeddings else 2)
         return layers * (attn + mlp + 2 * h) + embed + h
 
@@ -110,15 +155,44 @@ class ModelConfig:
                                         f"{rope['partial_rotary_factor']}) is not supported")
         if float(get("partial_rotary_factor", 1.0) or 1.0) != 1.0:
             raise UnsupportedModelError(f"{model_type}: partial rotary embedding is not supported")
-        if get("use_sliding_window", False) or (get("sliding_window") and model_type not in ("mistral",)):
-            raise UnsupportedModelError(f"{model_type}: sliding-window attention layers are not supported")
+        heads = int(get("num_attention_heads"))
+        layers = int(get("num_hidden_layers"))
+        extra: dict[str, Any] = {}
+        # per-layer attention kinds: transformers 5 writes layer_types; Mistral (and Qwen2 with use_sliding_window)
+        # express a window without them
+        window = int(get("sliding_window", 0) or 0)
+        kinds = list(get("layer_types", None) or [])
+        if model_type == "qwen2" and not get("use_sliding_window", False):
+            kinds, window = [], 0
+        if not kinds and window and model_type in ("mistral", "ministral"):
+            kinds = [SLIDING] * layers
+        if kinds and SLIDING in kinds:
+            extra.update(layer_types=tuple(kinds), sliding_window=window)
+        elif model_type != "qwen2" and get("use_sliding_window", False):
+            raise UnsupportedModelError(f"{model_type}: use_sliding_window without layer types is not supported")
+        # Gemma-3 keeps one rotary parameter set per layer kind
+        if isinstance(rope, dict) and isinstance(rope.get(FULL), dict):
+            local = rope.get(SLIDING)
+            rope = dict(rope[FULL])
+            if isinstance(local, dict):
+                extra["local_rope"] = dict(local)
         theta = get("rope_theta")
         if theta is None and isinstance(rope, dict):
             theta = rope.get("rope_theta")
         if isinstance(rope, dict) and rope.get("rope_type", rope.get("type", "default")) in ("default", None):
             rope = None
-        heads = int(get("num_attention_heads"))
-        extra: dict[str, Any] = {}
+        if model_type in ("gemma", "gemma2", "gemma3_text"):
+            act = get("hidden_activation") or get("hidden_act")
+            if act not in ("gelu_pytorch_tanh", "gelu_tanh"):
+                raise UnsupportedModelError(f"{model_type}: activation {act!r} is not supported")
+            extra.update(hidden_act="gelu_tanh", norm_unit_offset=True, embedding_multiplier_in_dtype=True,
+                         embedding_multiplier=float(get("hidden_size")) ** 0.5)
+            if model_type != "gemma":
+                qpas = get("query_pre_attn_scalar")
+                extra.update(sandwich_norm=True, attention_multiplier=float(qpas) ** -0.5 if qpas else None,
+                             attn_softcap=get("attn_logit_softcapping"), final_softcap=get("final_logit_softcapping"))
+        elif (get("hidden_act") or "silu") != "silu":
+            raise UnsupportedModelError(f"{model_type}: activation {get('hidden_act')!r} is not supported")
         experts = int(get("num_local_experts", 0) or get("num_experts", 0) or 0)
         ffn = int(get("intermediate_size"))
         if model_type == "qwen3_moe":
@@ -133,13 +207,22 @@ class ModelConfig:
                          residual_multiplier=float(get("residual_multiplier", 1.0)),
                          attention_multiplier=float(get("attention_multiplier", 1.0)),
                          logits_scaling=float(get("logits_scaling", 1.0)))
-        if model_type == "olmo2":
+        if model_type in ("olmo2", "olmo3"):
             extra.update(post_norm=True, qk_norm_full=True)
+        if model_type == "olmoe":
+            if get("clip_qkv"):
+                raise UnsupportedModelError("olmoe with clip_qkv is not supported")
+            extra.update(qk_norm_full=True)
+        if model_type == "qwen2_moe":
+            if int(get("decoder_sparse_step", 1) or 1) != 1 or list(get("mlp_only_layers", []) or []):
+                raise UnsupportedModelError("qwen2_moe with dense layers between the sparse ones is not supported")
+            ffn = int(get("moe_intermediate_size"))
+            extra["shared_expert_size"] = int(get("shared_expert_intermediate_size", 0) or 0)
         return cls(
             vocab_size=int(get("vocab_size")),
             hidden_size=int(get("hidden_size")),
             intermediate_size=ffn,
-            num_layers=int(get("num_hidden_layers")),
+            num_layers=layers,
             num_heads=heads,
             num_kv_heads=int(get("num_key_value_heads") or heads),
             head_dim=get("head_dim"),
@@ -148,8 +231,8 @@ class ModelConfig:
             rope_scaling=dict(rope) if isinstance(rope, dict) else None,
             max_position_embeddings=int(get("max_position_embeddings", 8192)),
             tie_word_embeddings=bool(get("tie_word_embeddings", False)),
-            attention_bias=bool(get("attention_bias", model_type == "qwen2")),
-            qk_norm=model_type in ("qwen3", "qwen3_moe", "olmo2"),
+            attention_bias=bool(get("attention_bias", model_type in ("qwen2", "qwen2_moe"))),
+            qk_norm=model_type in ("qwen3", "qwen3_moe", "olmo2", "olmo3", "olmoe", "gemma3_text"),
             num_experts=experts,
             experts_per_token=int(get("num_experts_per_tok", 2) or 2),
             model_type=model_type,
@@ -170,6 +253,41 @@ class ModelConfig:
         if self.rope_scaling is not None:
             common["rope_scaling"] = dict(self.rope_scaling)
         kind = self.model_type
+        kinds = dict(layer_types=list(self.layer_types), sliding_window=self.sliding_window) if self.layer_types \
+            else {}
+        if kind in ("gemma", "gemma2", "gemma3_text"):
+            gem = dict(hidden_activation="gelu_pytorch_tanh", **common)
+            if kind == "gemma":
+                return transformers.GemmaConfig(**gem)
+            gem.update(query_pre_attn_scalar=round((self.attention_multiplier or self.head_dim ** -0.5) ** -2),
+                       **kinds)
+            if kind == "gemma2":
+                return transformers.Gemma2Config(attn_logit_softcapping=self.attn_softcap,
+                                                 final_logit_softcapping=self.final_softcap, **gem)
+            full = {"rope_type": "default", "rope_theta": self.rope_theta, **(self.rope_scaling or {})}
+            local = {"rope_type": "default", "rope_theta": self.rope_theta, **(self.local_rope or {})}
+            gem.pop("rope_theta")
+            gem.pop("rope_scaling", None)
+            return transformers.Gemma3TextConfig(rope_parameters={FULL: full, SLIDING: local},
+                                                 attn_logit_softcapping=self.attn_softcap,
+                                                 final_logit_softcapping=self.final_softcap, **gem)
+        if kind == "ministral":
+            return transformers.MinistralConfig(**kinds, **{k: v for k, v in common.items() if k != "attention_bias"})
+        if kind == "mistral":
+            return transformers.MistralConfig(sliding_window=self.sliding_window or None,
+                                              **{k: v for k, v in common.items() if k != "attention_bias"})
+        if kind == "olmo3":
+            return transformers.Olmo3Config(**kinds, **{k: v for k, v in common.items() if k != "head_dim"})
+        if kind == "olmoe":
+            return transformers.OlmoeConfig(num_experts=self.num_experts, num_experts_per_tok=self.experts_per_token,
+                                            norm_topk_prob=self.norm_topk_prob,
+                                            **{k: v for k, v in common.items() if k != "head_dim"})
+        if kind == "qwen2_moe":
+            return transformers.Qwen2MoeConfig(num_experts=self.num_experts, num_experts_per_tok=self.experts_per_token,
+                                               moe_intermediate_size=self.intermediate_size,
+                                               shared_expert_intermediate_size=self.shared_expert_size,
+                                               norm_topk_prob=self.norm_topk_prob,
+                                               **{k: v for k, v in common.items() if k not in ("attention_bias",)})
         if kind == "qwen3_moe":
             return transformers.Qwen3MoeConfig(num_experts=self.num_experts, num_experts_per_tok=self.experts_per_token,
                                                moe_intermediate_size=self.intermediate_size,
@@ -194,17 +312,22 @@ class ModelConfig:
         if kind == "qwen3":
             return transformers.Qwen3Config(**common)
         if kind == "qwen2":
-            return transformers.Qwen2Config(**{k: v for k, v in common.items() if k != "attention_bias"})
+            window = dict(use_sliding_window=True, **kinds) if self.layer_types else {}
+            return transformers.Qwen2Config(**window, **{k: v for k, v in common.items() if k != "attention_bias"})
         return transformers.LlamaConfig(**common)
 
 
-def rope_inv_freq(config: ModelConfig) -> torch.Tensor:
+def rope_inv_freq(config: ModelConfig, local: bool = False) -> torch.Tensor:
     """Inverse frequencies ``[D/2]`` (fp32) of the rotary embedding, with Llama-3 frequency scaling when
     ``rope_scaling`` says so (the published Llama 3.1 rule: long wavelengths divided by ``factor``, short ones
-    kept, a linear blend of the two in between)."""
+    kept, a linear blend of the two in between). ``local``: the sliding-window layers' parameters
+    (``config.local_rope``)."""
     dim = config.head_dim
-    inv = 1.0 / (config.rope_theta ** (torch.arange(0, dim, 2, dtype=torch.int64).float() / dim))
-    scaling = config.rope_scaling or {}
+    theta, scaling = config.rope_theta, config.rope_scaling or {}
+    if local and config.local_rope is not None:
+        theta = float(config.local_rope.get("rope_theta", theta))
+        scaling = {k: v for k, v in config.local_rope.items() if k != "rope_theta"}
+    inv = 1.0 / (theta ** (torch.arange(0, dim, 2, dtype=torch.int64).float() / dim))
     kind = scaling.get("rope_type", scaling.get("type"))
     if kind == "llama3":
         factor = float(scaling["factor"])

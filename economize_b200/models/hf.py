@@ -1,5 +1,8 @@
 """Conversion between Hugging Face state dicts and the engine's fused parameter layout.
 
+Gemma's RMSNorm weights ``w`` (the norm scales by ``1 + w``) are stored as ``1 + w`` here, so every family runs the
+same norm kernel; sandwich blocks (Gemma-2/3) map four norms per block.
+
 Names follow ``transformers`` 5 (``model.layers.{i}.self_attn.q_proj.weight`` ..., Mixtral experts as fused
 ``mlp.experts.gate_up_proj [E, 2F, H]`` / ``down_proj [E, H, F]``; the older per-expert ``block_sparse_moe.experts.
 {e}.w1/w2/w3`` layout is read too).
@@ -20,12 +23,21 @@ def _take(state: dict[str, torch.Tensor], key: str) -> torch.Tensor:
     return state[key]
 
 
+def _norm_in(config, w: torch.Tensor) -> torch.Tensor:
+    """A checkpoint's RMSNorm weight as this model stores it (Gemma checkpoints store ``w`` of ``1 + w``)."""
+    return w.float() + 1.0 if config.norm_unit_offset else w
+
+
+def _norm_out(config, w: torch.Tensor) -> torch.Tensor:
+    return (w.detach().float() - 1.0).to(w.dtype) if config.norm_unit_offset else w.detach()
+
+
 @torch.no_grad()
 def load_hf_state(model, state: dict[str, torch.Tensor]) -> None:
     """Copy a Hugging Face state dict into ``model`` (a :class:`~economize_b200.models.CausalLM`)."""
     c = model.config
     model.embed.copy_(_take(state, "model.embed_tokens.weight"))
-    model.norm.copy_(_take(state, "model.norm.weight"))
+    model.norm.copy_(_norm_in(c, _take(state, "model.norm.weight")))
     if model.lm_head is not None:
         model.lm_head.copy_(state.get("lm_head.weight", state["model.embed_tokens.weight"]))
     for i, layer in enumerate(model.layers):
@@ -39,19 +51,23 @@ def load_hf_state(model, state: dict[str, torch.Tensor]) -> None:
             layer.bqkv.copy_(torch.cat([_take(state, a + f"{n}_proj.bias") for n in "qkv"], 0))
         layer.wo.copy_(_take(state, a + "o_proj.weight"))
         if layer.q_norm is not None:
-            layer.q_norm.copy_(_take(state, a + "q_norm.weight"))
-            layer.k_norm.copy_(_take(state, a + "k_norm.weight"))
-        if c.post_norm:  # olmo2: the norms follow the branches (attn_norm / mlp_norm hold them)
-            layer.attn_norm.copy_(_take(state, p + "post_attention_layernorm.weight"))
-            layer.mlp_norm.copy_(_take(state, p + "post_feedforward_layernorm.weight"))
-        else:
-            layer.attn_norm.copy_(_take(state, p + "input_layernorm.weight"))
-            layer.mlp_norm.copy_(_take(state, p + "post_attention_layernorm.weight"))
+            layer.q_norm.copy_(_norm_in(c, _take(state, a + "q_norm.weight")))
+            layer.k_norm.copy_(_norm_in(c, _take(state, a + "k_norm.weight")))
+        for ours, theirs in _norm_names(c):
+            getattr(layer, ours).copy_(_norm_in(c, _take(state, p + theirs + ".weight")))
+        if layer.sinks is not None and a + "sinks" in state:
+            layer.sinks.copy_(state[a + "sinks"])
         if c.is_moe:
             if p + "mlp.experts.gate_up_proj" in state:
                 layer.router.copy_(_take(state, p + "mlp.gate.weight"))
                 layer.w_gate_up.copy_(state[p + "mlp.experts.gate_up_proj"])
                 layer.w_down.copy_(_take(state, p + "mlp.experts.down_proj"))
+                if layer.w_shared_gate_up is not None:  # qwen2_moe
+                    x = p + "mlp.shared_expert."
+                    layer.w_shared_gate_up.copy_(torch.cat([_take(state, x + "gate_proj.weight"),
+                                                            _take(state, x + "up_proj.weight")], 0))
+                    layer.w_shared_down.copy_(_take(state, x + "down_proj.weight"))
+                    layer.shared_gate.copy_(_take(state, p + "mlp.shared_expert_gate.weight"))
             else:
                 m = p + "block_sparse_moe."
                 layer.router.copy_(_take(state, m + "gate.weight"))
@@ -70,6 +86,16 @@ def load_hf_state(model, state: dict[str, torch.Tensor]) -> None:
             layer.w_down.copy_(_take(state, m + "down_proj.weight"))
 
 
+def _norm_names(config) -> list[tuple[str, str]]:
+    """(this model's parameter, the checkpoint's name) of a block's norms."""
+    if config.sandwich_norm:  # gemma2 / gemma3: a norm before and after each branch
+        return [("attn_norm", "input_layernorm"), ("attn_post_norm", "post_attention_layernorm"),
+                ("mlp_norm", "pre_feedforward_layernorm"), ("mlp_post_norm", "post_feedforward_layernorm")]
+    if config.post_norm:  # olmo2 / olmo3: the norms follow the branches (attn_norm / mlp_norm hold them)
+        return [("attn_norm", "post_attention_layernorm"), ("mlp_norm", "post_feedforward_layernorm")]
+    return [("attn_norm", "input_layernorm"), ("mlp_norm", "post_attention_layernorm")]
+
+
 @torch.no_grad()
 def export_hf_state(model, copy: bool = True) -> dict[str, torch.Tensor]:
     """The Hugging Face state dict of ``model`` (split projections, ``transformers`` 5 names); quantized projections
@@ -83,7 +109,7 @@ def export_hf_state(model, copy: bool = True) -> dict[str, torch.Tensor]:
             return t.dequantize()
         return t.detach()
 
-    out = {"model.embed_tokens.weight": model.embed.detach(), "model.norm.weight": model.norm.detach()}
+    out = {"model.embed_tokens.weight": model.embed.detach(), "model.norm.weight": _norm_out(c, model.norm)}
     if model.lm_head is not None:
         out["lm_head.weight"] = model.lm_head.detach()
     for i, layer in enumerate(model.layers):
@@ -99,18 +125,22 @@ def export_hf_state(model, copy: bool = True) -> dict[str, torch.Tensor]:
                 out[p + f"self_attn.{n}_proj.bias"] = w
         out[p + "self_attn.o_proj.weight"] = full(layer.wo)
         if layer.q_norm is not None:
-            out[p + "self_attn.q_norm.weight"] = layer.q_norm.detach()
-            out[p + "self_attn.k_norm.weight"] = layer.k_norm.detach()
-        if c.post_norm:
-            out[p + "post_attention_layernorm.weight"] = layer.attn_norm.detach()
-            out[p + "post_feedforward_layernorm.weight"] = layer.mlp_norm.detach()
-        else:
-            out[p + "input_layernorm.weight"] = layer.attn_norm.detach()
-            out[p + "post_attention_layernorm.weight"] = layer.mlp_norm.detach()
+            out[p + "self_attn.q_norm.weight"] = _norm_out(c, layer.q_norm)
+            out[p + "self_attn.k_norm.weight"] = _norm_out(c, layer.k_norm)
+        for ours, theirs in _norm_names(c):
+            out[p + theirs + ".weight"] = _norm_out(c, getattr(layer, ours))
+        if layer.sinks is not None:
+            out[p + "self_attn.sinks"] = layer.sinks.detach()
         if c.is_moe:
             out[p + "mlp.gate.weight"] = layer.router.detach()
             out[p + "mlp.experts.gate_up_proj"] = full(layer.w_gate_up)
             out[p + "mlp.experts.down_proj"] = full(layer.w_down)
+            if layer.w_shared_gate_up is not None:
+                g, u = full(layer.w_shared_gate_up).chunk(2, 0)
+                out[p + "mlp.shared_expert.gate_proj.weight"] = g
+                out[p + "mlp.shared_expert.up_proj.weight"] = u
+                out[p + "mlp.shared_expert.down_proj.weight"] = full(layer.w_shared_down)
+                out[p + "mlp.shared_expert_gate.weight"] = layer.shared_gate.detach()
         elif c.model_type == "phi3":
             out[p + "mlp.gate_up_proj.weight"] = full(layer.w_gate_up)
             out[p + "mlp.down_proj.weight"] = full(layer.w_down)

@@ -1,4 +1,5 @@
-"""The engine's own decoder executor for Llama-family models (Llama, Mistral, Qwen2, Qwen3, and Mixtral-style MoE).
+"""The engine's own decoder executor for Llama-family models (Llama, Mistral, Qwen2, Qwen3, Mixtral-style MoE, and the
+variants ``ModelConfig`` describes: Gemma's GeGLU and sandwich norms, soft-caps, sliding windows, shared experts).
 
 Weights are stored fused for the GEMM kernels: ``wqkv = [W_q; W_k; W_v]`` and ``w_gate_up = [W_gate; W_up]`` (one
 read of the activations per projection group), in contrast to economize, which calls the Hugging Face decoder layers
@@ -47,6 +48,16 @@ class DecoderLayer(nn.Module):
         self.q_norm = nn.Parameter(torch.ones(qn, **kw)) if config.qk_norm else None
         self.k_norm = nn.Parameter(torch.ones(kn, **kw)) if config.qk_norm else None
         self.mlp_norm = nn.Parameter(torch.ones(h, **kw))
+        # sandwich blocks (Gemma-2/3): attn_norm / mlp_norm precede the branches, these follow them
+        self.attn_post_norm = nn.Parameter(torch.ones(h, **kw)) if config.sandwich_norm else None
+        self.mlp_post_norm = nn.Parameter(torch.ones(h, **kw)) if config.sandwich_norm else None
+        # Qwen2-MoE: a dense shared expert next to the routed ones, gated by sigmoid(x . shared_gate)
+        se = config.shared_expert_size if config.is_moe else 0
+        self.w_shared_gate_up = nn.Parameter(torch.empty(2 * se, h, **kw)) if se else None
+        self.w_shared_down = nn.Parameter(torch.empty(h, se, **kw)) if se else None
+        self.shared_gate = nn.Parameter(torch.empty(1, h, **kw)) if se else None
+        #: attention sink logits of this layer's query heads (fp32 [H]; gpt-oss-style models), or None
+        self.sinks = None
         if config.is_moe:
             e = config.num_experts
             self.router = nn.Parameter(torch.empty(e, h, **kw))
@@ -78,6 +89,7 @@ class CausalLM(nn.Module):
         self.lm_head = None if config.tie_word_embeddings else nn.Parameter(
             torch.empty(config.vocab_size, config.hidden_size, **kw))
         self._rope: tuple[torch.Tensor, torch.Tensor] | None = None
+        self._rope_local: tuple[torch.Tensor, torch.Tensor] | None = None
         #: calibration hook ``observer(layer, name, x)`` called with the input of every projection (or None)
         self.observer = None
         #: KV-cache storage set by KV techniques: dtype (None: the compute dtype) and fp8 scales ([L, H_kv] x 2)
@@ -111,16 +123,32 @@ class CausalLM(nn.Module):
     def head_weight(self) -> torch.Tensor:
         return self.embed if self.lm_head is None else self.lm_head
 
-    def rope_tables(self, length: int | None = None) -> tuple[torch.Tensor, torch.Tensor]:
+    def rope_tables(self, length: int | None = None, local: bool = False) -> tuple[torch.Tensor, torch.Tensor]:
         """``cos, sin [P, D/2]`` fp32 for positions ``0..P-1`` (computed once per device, like HF: the angle is the
-        fp32 product of the position and the inverse frequency)."""
+        fp32 product of the position and the inverse frequency). ``local``: the tables of the sliding-window layers
+        when their rotary parameters differ (Gemma-3)."""
         need = max(length or 0, self.config.max_position_embeddings)
-        if self._rope is None or self._rope[0].shape[0] < need or self._rope[0].device != self.device:
-            inv = rope_inv_freq(self.config).to(self.device)
+        local = local and self.config.local_rope is not None
+        cached = self._rope_local if local else self._rope
+        if cached is None or cached[0].shape[0] < need or cached[0].device != self.device:
+            inv = rope_inv_freq(self.config, local=local).to(self.device)
             pos = torch.arange(need, device=self.device, dtype=torch.float32)
             angles = pos[:, None] * inv[None, :]
-            self._rope = (angles.cos().contiguous(), angles.sin().contiguous())
-        return self._rope
+            cached = (angles.cos().contiguous(), angles.sin().contiguous())
+            if local:
+                self._rope_local = cached
+            else:
+                self._rope = cached
+        return cached
+
+    def _layer_rope(self, index: int, cos: torch.Tensor, sin: torch.Tensor) -> tuple[torch.Tensor, torch.Tensor]:
+        """The rotary tables layer ``index`` uses: none (NoPE), the sliding layers' own, or the model's."""
+        c = self.config
+        if index in c.nope_layers:
+            return self._identity_rope(cos)
+        if c.local_rope is not None and c.window_of(index):
+            return self.rope_tables(cos.shape[0], local=True)
+        return cos, sin
 
     def new_cache(self, batch: int, capacity: int) -> KVCache:
         """A zeroed cache in the model's KV format (``kv_dtype``: the compute dtype, or fp8 e4m3 with the per-head
@@ -138,7 +166,11 @@ class CausalLM(nn.Module):
     def embed_tokens(self, tokens: torch.Tensor) -> torch.Tensor:
         h = self.embed[tokens]
         m = self.config.embedding_multiplier
-        return h if m == 1.0 else h * m
+        if m == 1.0:
+            return h
+        if self.config.embedding_multiplier_in_dtype:  # Gemma multiplies by the normalizer rounded to the dtype
+            return h * torch.tensor(m, dtype=h.dtype)
+        return h * m
 
     def _identity_rope(self, cos: torch.Tensor) -> tuple[torch.Tensor, torch.Tensor]:
         """cos = 1, sin = 0 tables of ``cos``'s shape: rotary embedding that leaves q and k unchanged (NoPE)."""
@@ -162,7 +194,7 @@ class CausalLM(nn.Module):
             return sparse.chunked_forward(self, tokens, batch, cache, capture)
         if self._sequence_parallel(tokens, layers, hidden):
             return self._forward_sp(tokens, batch, cache, capture)
-        if c.post_norm:
+        if c.post_norm or c.sandwich_norm:
             return self._forward_post_norm(tokens, batch, cache, capture, layers, hidden)
         cos, sin = self.rope_tables()
         h = self.embed_tokens(tokens) if hidden is None else hidden
@@ -217,21 +249,25 @@ class CausalLM(nn.Module):
 
     def _forward_post_norm(self, tokens: torch.Tensor, batch: StepBatch, cache: KVCache, capture: tuple[int, ...],
                            layers: range | None, hidden: torch.Tensor | None):
-        """:meth:`forward_step` for blocks whose norms follow the branches (OLMo-2):
-        ``h = h + norm(attn(h)); h = h + norm(mlp(h))``, then the final norm."""
+        """:meth:`forward_step` for blocks whose norms follow the branches: ``h = h + norm(attn(h)); h = h +
+        norm(mlp(h))`` (OLMo-2/3), or with a norm before each branch too, ``h = h + post(attn(pre(h)))`` (Gemma-2/3),
+        then the final norm."""
         c = self.config
         eps = c.rms_norm_eps
         cos, sin = self.rope_tables()
         h = self.embed_tokens(tokens) if hidden is None else hidden
         aux: dict[int, torch.Tensor] = {}
+        sandwich = c.sandwich_norm
         for i in (layers if layers is not None else range(c.num_layers)):
             layer = self.layers[i]
             if i in capture:
                 aux[i] = h
-            a = self._materialize(self._attention(layer, i, h, batch, cache, cos, sin), True)
-            h = h + ops.rmsnorm(a, layer.attn_norm, eps)[0]
-            m = self._materialize(self._mlp(layer, h, i), True)
-            h = h + ops.rmsnorm(m, layer.mlp_norm, eps)[0]
+            x = ops.rmsnorm(h, layer.attn_norm, eps)[0] if sandwich else h
+            a = self._materialize(self._attention(layer, i, x, batch, cache, cos, sin), True)
+            h = h + ops.rmsnorm(a, layer.attn_post_norm if sandwich else layer.attn_norm, eps)[0]
+            x = ops.rmsnorm(h, layer.mlp_norm, eps)[0] if sandwich else h
+            m = self._materialize(self._mlp(layer, x, i), True)
+            h = h + ops.rmsnorm(m, layer.mlp_post_norm if sandwich else layer.mlp_norm, eps)[0]
         out = ops.rmsnorm(h, self.norm, eps)[0]
         if c.num_layers in capture or -2 in capture:
             aux[c.num_layers] = aux[-2] = h
@@ -249,7 +285,8 @@ class CausalLM(nn.Module):
             return False
         c = self.config
         if c.is_moe or self.observer is not None or self.depth_policy is not None or c.post_norm or \
-                c.qk_norm_full or c.residual_multiplier != 1.0:
+                c.qk_norm_full or c.residual_multiplier != 1.0 or c.sandwich_norm or c.hidden_act != "silu" or \
+                c.final_softcap:
             return False
         return not any(getattr(layer, name, None) for layer in self.layers
                        for name in ("skip_attn", "skip_mlp", "mlp_rule", "attn_input_hook"))
@@ -352,8 +389,7 @@ class CausalLM(nn.Module):
             k_part = ops.rmsnorm(k_part.contiguous(), k_norm, c.rms_norm_eps)[0]
             qkv = torch.cat([q_part, k_part, v_part], -1)
             q_norm = k_norm = None
-        if index in c.nope_layers:
-            cos, sin = self._identity_rope(cos)
+        cos, sin = self._layer_rope(index, cos, sin)
         q = ops.rope_store(qkv, batch.positions, cos, sin, self.local["num_heads"], self.local["num_kv_heads"],
                            c.head_dim, k_cache,
                            v_cache, batch.kv_len, batch.n_new, q_norm, k_norm, c.rms_norm_eps,
@@ -368,7 +404,8 @@ class CausalLM(nn.Module):
         sparse_pass = sparse is not None and sparse.active
         tail = self.exact_tail if (not batch.prompt and q.shape[1] <= 64 and not sparse_pass) else 0
         o = ops.attention(q, k_cache, v_cache, batch.kv_len, batch.n_new, batch.mask, scale=c.attention_multiplier,
-                          q_offset=batch.q_offset, k_scale=k_scale, v_scale=v_scale, keep=keep, tail=tail, **kivi)
+                          q_offset=batch.q_offset, k_scale=k_scale, v_scale=v_scale, keep=keep, tail=tail,
+                          softcap=c.attn_softcap, sinks=layer.sinks, window=c.window_of(index), **kivi)
         if self.kv_evictor is not None and batch.is_prefill:
             self.kv_evictor.observe_prefill(index, q, k_cache, v_cache, batch)
         return o.reshape(*o.shape[:2], -1)
@@ -394,8 +431,13 @@ class CausalLM(nn.Module):
         if layer.router is not None:
             from ..parallel.moe import moe_mlp
 
-            return moe_mlp(x, layer.router, layer.w_gate_up, layer.w_down, self.config.experts_per_token,
-                           getattr(self, "ep", None), renormalize=self.config.norm_topk_prob)
+            out = moe_mlp(x, layer.router, layer.w_gate_up, layer.w_down, self.config.experts_per_token,
+                          getattr(self, "ep", None), renormalize=self.config.norm_topk_prob)
+            if layer.w_shared_gate_up is not None:  # Qwen2-MoE's gated shared expert
+                shared = ops.linear(ops.silu_mul(ops.linear(x, layer.w_shared_gate_up)), layer.w_shared_down)
+                gate = torch.sigmoid(ops.linear(x, layer.shared_gate))
+                out = out + gate * shared
+            return out
         if self.observer is not None:
             self.observer(index, "w_gate_up", x)
         rule = getattr(layer, "mlp_rule", None)  # activation-sparse MLPs (CATS, Deja Vu); None: the dense path
@@ -403,7 +445,7 @@ class CausalLM(nn.Module):
             out = rule(self, layer, x, index)
             if out is not None:
                 return out
-        a = ops.silu_mul(self._linear(x, layer.w_gate_up))
+        a = ops.glu(self._linear(x, layer.w_gate_up), self.config.hidden_act)
         if self.observer is not None:
             self.observer(index, "w_down", a)
         return self._row_linear(a, layer.w_down)
@@ -420,7 +462,7 @@ class CausalLM(nn.Module):
 
     def logits(self, hidden: torch.Tensor) -> torch.Tensor:
         """Logits over the full vocabulary (gathered from the vocabulary shards under tensor parallelism)."""
-        local = ops.linear(hidden, self.head_weight)
+        local = self._soft_cap(ops.linear(hidden, self.head_weight))
         scale = self.config.logits_scaling
         if scale != 1.0:  # Granite divides its logits (a positive scale: the argmax is unchanged)
             local = local / scale
@@ -429,10 +471,18 @@ class CausalLM(nn.Module):
         every = self.tp.all_gather(local)  # [P, ..., V/P]
         return torch.cat(list(every.unbind(0)), -1)
 
+    def _soft_cap(self, logits: torch.Tensor) -> torch.Tensor:
+        """Gemma-2's final-logit soft-cap ``cap * tanh(logits / cap)`` (in the logits' dtype, as HF computes it)."""
+        cap = self.config.final_softcap
+        if not cap:
+            return logits
+        return torch.tanh(logits / cap) * cap
+
     def greedy(self, hidden: torch.Tensor) -> torch.Tensor:
         """Argmax token after every row of ``hidden`` (distributed over vocabulary shards under TP, without
         gathering the logits)."""
-        local = ops.linear(hidden, self.head_weight)
+        # the soft-cap is monotonic, but its rounding can tie two logits, and the first of a tie wins
+        local = self._soft_cap(ops.linear(hidden, self.head_weight))
         if self.tp is None or self.tp.size == 1:
             return ops.argmax(local)
         from ..parallel.tp import tp_argmax

@@ -38,6 +38,8 @@ __all__ = [
     "topk_logp",
     "tree_layout",
     "silu_mul",
+    "gelu_tanh_mul",
+    "glu",
 ]
 
 
@@ -125,29 +127,34 @@ def attention(q: torch.Tensor, k_cache: torch.Tensor, v_cache: torch.Tensor, kv_
               q_offset: int = 0, k_scale: torch.Tensor | None = None,
               v_scale: torch.Tensor | None = None, keep: torch.Tensor | None = None,
               lse_out: torch.Tensor | None = None, kivi: torch.Tensor | None = None,
-              kivi_chunks: torch.Tensor | None = None, kivi_bits: int = 0, tail: int = 0) -> torch.Tensor:
+              kivi_chunks: torch.Tensor | None = None, kivi_bits: int = 0, tail: int = 0,
+              softcap: float | None = None, sinks: torch.Tensor | None = None, window: int = 0) -> torch.Tensor:
     """Causal / tree-masked attention over the slot cache (see :func:`.reference.attention`); fp8 caches take
     per-KV-head scales, ``keep`` (int32 bit words ``[B, H_kv, S / 32]``) hides evicted committed slots and
-    ``lse_out [B, T, H]`` receives every row's log2-domain log-sum-exp.
+    ``lse_out [B, T, H]`` receives every row's log2-domain log-sum-exp. ``softcap`` (tanh soft-capping of the
+    scores), ``sinks`` (fp32 ``[H]`` sink logits) and ``window`` (sliding window in positions; the kernel then reads
+    only the window's chunks) serve Gemma-2, gpt-oss and the sliding-window layers of Mistral, Gemma-2/3 and OLMo-3.
 
     ``tail > 0`` (passes of at most 64 queries) reduces the keys at the last ``tail`` positions before each query,
     and its own new keys, one at a time in position order: a verification pass then computes every query bit for
     bit as a one-token pass at the same position does, for trees up to ``tail`` deep (the CPU path computes the
     same values without that rounding guarantee)."""
     scale = float(scale if scale is not None else q.shape[-1] ** -0.5)
-    _trace_attention(q, k_cache, mask, k_scale, keep, kivi, tail)
+    window = int(window or 0)
+    _trace_attention(q, k_cache, mask, k_scale, keep, kivi, tail, softcap, sinks, window)
     if q.is_cuda:
         return require().attention(q, k_cache, v_cache, kv_len, n_new, mask, scale, int(q_offset), None, k_scale,
-                                   v_scale, keep, lse_out, kivi, kivi_chunks, int(kivi_bits), int(tail))
-    return reference.attention(q, k_cache, v_cache, kv_len, n_new, mask, scale, q_offset=q_offset, k_scale=k_scale,
-                               v_scale=v_scale, keep=keep, lse_out=lse_out, kivi=kivi, kivi_chunks=kivi_chunks,
-                               kivi_bits=kivi_bits)
+                                   v_scale, keep, lse_out, kivi, kivi_chunks, int(kivi_bits), int(tail),
+                                   float(softcap or 0.0), sinks, window)
+    return reference.attention(q, k_cache, v_cache, kv_len, n_new, mask, scale, softcap=softcap, q_offset=q_offset,
+                               k_scale=k_scale, v_scale=v_scale, keep=keep, lse_out=lse_out, kivi=kivi,
+                               kivi_chunks=kivi_chunks, kivi_bits=kivi_bits, sinks=sinks, window=window)
 
 
 _ATTENTION_USAGE: dict[tuple[str, str, int, str], int] = {}
 
 
-def _trace_attention(q, k_cache, mask, k_scale, keep, kivi, tail) -> None:
+def _trace_attention(q, k_cache, mask, k_scale, keep, kivi, tail, softcap=None, sinks=None, window=0) -> None:
     device = "cuda" if q.is_cuda else "cpu"
     cache = "kivi" if kivi is not None else "fp8" if k_scale is not None else str(k_cache.dtype).removeprefix("torch.")
     parts = ["masked" if mask is not None else "causal"]
@@ -155,6 +162,12 @@ def _trace_attention(q, k_cache, mask, k_scale, keep, kivi, tail) -> None:
         parts.append("exact_tail")
     if keep is not None:
         parts.append("keep")
+    if softcap:
+        parts.append("softcap")
+    if sinks is not None:
+        parts.append("sinks")
+    if window:
+        parts.append("window")
     key = (device, cache, int(q.shape[1]), "+".join(parts))
     _ATTENTION_USAGE[key] = _ATTENTION_USAGE.get(key, 0) + 1
 
@@ -193,6 +206,22 @@ def silu_mul(gate_up: torch.Tensor | Partials) -> torch.Tensor:
     if gate_up.is_cuda:
         return require().silu_mul(_raw(gate_up))
     return reference.silu_mul(gate_up)
+
+
+def gelu_tanh_mul(gate_up: torch.Tensor | Partials) -> torch.Tensor:
+    """``gelu_tanh(gate) * up`` of a fused ``[gate; up]`` projection (GeGLU)."""
+    if gate_up.is_cuda:
+        return require().glu(_raw(gate_up), 1)
+    return reference.gelu_tanh_mul(gate_up.sum() if isinstance(gate_up, Partials) else gate_up)
+
+
+def glu(gate_up: torch.Tensor | Partials, act: str = "silu") -> torch.Tensor:
+    """The gated MLP activation ``act(gate) * up`` (``"silu"``: SwiGLU, ``"gelu_tanh"``: GeGLU)."""
+    if act == "silu":
+        return silu_mul(gate_up)
+    if act == "gelu_tanh":
+        return gelu_tanh_mul(gate_up)
+    raise ValueError(f"unsupported gated activation {act!r}")
 
 
 def linear(x: torch.Tensor, weight, bias: torch.Tensor | None = None) -> torch.Tensor:

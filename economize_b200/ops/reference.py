@@ -76,8 +76,25 @@ def rope_store(qkv: torch.Tensor, positions: torch.Tensor, cos: torch.Tensor, si
 
 
 def visible_mask(kv_len: torch.Tensor, n_new: torch.Tensor, length: int, width: int,
-                 mask: torch.Tensor | None, q_offset: int = 0) -> torch.Tensor:
-    """Boolean ``[B, T, width]`` visibility of cache slots for the queries of a pass (see :func:`attention`)."""
+                 mask: torch.Tensor | None, q_offset: int = 0, window: int = 0) -> torch.Tensor:
+    """Boolean ``[B, T, width]`` visibility of cache slots for the queries of a pass (see :func:`attention`).
+    ``window > 0`` also hides the slots below ``position - window + 1`` (the query's position is the committed length
+    plus its tree depth, or plus its index among the new tokens without a tree)."""
+    vis = _visible(kv_len, n_new, length, width, mask, q_offset)
+    if window > 0:
+        t = torch.arange(length, device=kv_len.device)
+        if mask is None:
+            depth = (q_offset + t)[None, :].expand(kv_len.shape[0], length)
+        else:
+            ones = ((mask.long()[..., None] >> torch.arange(64, device=mask.device)) & 1).sum(-1)
+            depth = (ones - 1).clamp_min(0)
+        lo = kv_len.long()[:, None] + depth - window + 1  # [B, T]
+        vis = vis & (torch.arange(width, device=kv_len.device)[None, None, :] >= lo[:, :, None])
+    return vis
+
+
+def _visible(kv_len: torch.Tensor, n_new: torch.Tensor, length: int, width: int,
+             mask: torch.Tensor | None, q_offset: int = 0) -> torch.Tensor:
     device = kv_len.device
     slots = torch.arange(width, device=device)
     t = torch.arange(length, device=device)
@@ -99,18 +116,21 @@ def attention(q: torch.Tensor, k_cache: torch.Tensor, v_cache: torch.Tensor, kv_
               softcap: float | None = None, q_offset: int = 0, k_scale: torch.Tensor | None = None,
               v_scale: torch.Tensor | None = None, keep: torch.Tensor | None = None,
               lse_out: torch.Tensor | None = None, kivi: torch.Tensor | None = None,
-              kivi_chunks: torch.Tensor | None = None, kivi_bits: int = 0) -> torch.Tensor:
+              kivi_chunks: torch.Tensor | None = None, kivi_bits: int = 0, sinks: torch.Tensor | None = None,
+              window: int = 0) -> torch.Tensor:
     """Attention of queries ``[B, T, H, D]`` over the slot cache ``[B, H_kv, S, D]`` (bf16, fp32, or e4m3 codes with
     per-KV-head scales ``k_scale``/``v_scale``).
 
     Query ``t`` of row ``b`` sees every committed slot ``< kv_len[b]`` and the new tokens' slots ``kv_len[b] + j``
     (``j < n_new[b]``) for which bit ``j`` of ``mask[b, t]`` is set (``mask=None``: causal, ``j <= q_offset + t``).
-    Heads are grouped: query head ``h`` reads KV head ``h // (H / H_kv)``.
+    Heads are grouped: query head ``h`` reads KV head ``h // (H / H_kv)``. ``softcap`` maps every scaled score ``s``
+    to ``softcap * tanh(s / softcap)``; ``sinks [H]`` adds one logit per query head to the softmax denominator (it
+    carries no value); ``window`` hides keys more than ``window - 1`` positions behind the query.
     """
     batch, length, heads, dim = q.shape
     kv_heads = k_cache.shape[1]
     width = max(int((kv_len + n_new).max()), 1)
-    vis = visible_mask(kv_len, n_new, length, width, mask, q_offset)  # [B, T, W]
+    vis = visible_mask(kv_len, n_new, length, width, mask, q_offset, window)  # [B, T, W]
     keys = k_cache[:, :, :width].float()
     values = v_cache[:, :, :width].float()
     if k_scale is not None:
@@ -138,6 +158,10 @@ def attention(q: torch.Tensor, k_cache: torch.Tensor, v_cache: torch.Tensor, kv_
         committed = torch.arange(width, device=keep.device)[None, :] < kv_len.long()[:, None]  # [B, W]
         vis = vis & (kept | ~committed[:, None])[:, :, None, :]
     scores = scores.masked_fill(~vis, float("-inf"))
+    if sinks is not None:  # one extra logit per query head that joins the denominator only
+        sink = sinks.float()[None, :, None, None].expand(batch, heads, length, 1)
+        scores = torch.cat([scores, sink], -1)
+        values = torch.cat([values, values.new_zeros(*values.shape[:2], 1, dim)], 2)
     if lse_out is not None:  # log2-domain log-sum-exp per (row, token, head), like the kernel's
         lse = torch.logsumexp(scores, -1) * 1.4426950408889634  # [B, H, T]
         lse_out.copy_(lse.transpose(1, 2))
@@ -150,6 +174,12 @@ def silu_mul(gate_up: torch.Tensor) -> torch.Tensor:
     """``silu(gate) * up`` for ``gate_up = [..., 2F]`` holding the gate first (rounded like HF's Llama MLP)."""
     gate, up = gate_up.chunk(2, -1)
     return F.silu(gate) * up
+
+
+def gelu_tanh_mul(gate_up: torch.Tensor) -> torch.Tensor:
+    """``gelu_tanh(gate) * up`` (Gemma's GeGLU MLP, rounded like HF's)."""
+    gate, up = gate_up.chunk(2, -1)
+    return F.gelu(gate, approximate="tanh") * up
 
 
 def linear(x: torch.Tensor, weight: torch.Tensor, bias: torch.Tensor | None = None) -> torch.Tensor:

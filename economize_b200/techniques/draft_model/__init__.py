@@ -16,30 +16,46 @@ from ...errors import ConfigError
 from ...models.llama import CausalLM
 from ...runtime.cache import KVCache, StepBatch
 
-__all__ = ["DraftLMDrafter", "DraftModelConfig", "DraftModelTechnique", "load_draft"]
+__all__ = ["DraftLMDrafter", "DraftModelConfig", "DraftModelTechnique", "install_view", "load_draft"]
 
 
 @dataclass(frozen=True)
 class DraftModelConfig(TechniqueConfig):
     """Attributes: ``model`` (a Hugging Face id or path, a ``transformers`` causal LM or an engine
     :class:`CausalLM`), ``revision``, ``dtype`` (``None``: the target's), ``attn_implementation`` (accepted for
-    compatibility; the engine's kernels run the model)."""
+    compatibility; the engine's kernels run the model), ``window`` / ``sink`` (``window > 0``: the draft model
+    attends to a StreamingLLM view of its own cache, the first ``sink`` prompt tokens plus the ``window`` most
+    recent ones, as TriForce's and MagicDec's long-context drafters do; the attention kernel skips the hidden
+    128-key chunks)."""
 
     technique: ClassVar[str] = "draft_model"
     model: Any = None
     revision: str | None = None
     dtype: str | None = None
     attn_implementation: str | None = None
+    window: int = 0
+    sink: int = 0
 
     def __post_init__(self) -> None:
         if self.model is None:
             raise ConfigError("draft_model needs model= (an id, a path or a model)")
+        if self.window < 0 or self.sink < 0:
+            raise ConfigError("draft_model window and sink must be >= 0")
 
     def to_dict(self) -> dict[str, Any]:
         out = {f.name: getattr(self, f.name) for f in fields(self)}
         if not isinstance(out["model"], str):
             out["model"] = getattr(getattr(self.model, "config", None), "_name_or_path", None) or "<in-memory model>"
         return out
+
+
+def install_view(draft: CausalLM, config: DraftModelConfig) -> None:
+    """With ``config.window > 0`` the draft model attends to a StreamingLLM view of its own cache."""
+    if config.window > 0:
+        from ..sparse_kv_draft import MagicDecConfig, SparseViewEvictor
+
+        draft.kv_evictor = SparseViewEvictor(MagicDecConfig(sink=config.sink, window=config.window),
+                                             draft.config.num_layers)
 
 
 def load_draft(config: DraftModelConfig, target: CausalLM) -> CausalLM:
@@ -71,6 +87,7 @@ class DraftModelTechnique(Technique):
     def __init__(self, config: DraftModelConfig, model: CausalLM) -> None:
         super().__init__(config, model)
         self._draft = [load_draft(config, model)]  # not a submodule: its weights are not the technique's
+        install_view(self.draft, config)
 
     @property
     def draft(self) -> CausalLM:

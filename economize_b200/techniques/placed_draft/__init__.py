@@ -13,7 +13,7 @@ import torch
 from ...core.technique import register_technique
 from ...decoding.config import DecodeConfig
 from ...errors import ConfigError
-from ..draft_model import DraftLMDrafter, DraftModelConfig, DraftModelTechnique, load_draft
+from ..draft_model import DraftLMDrafter, DraftModelConfig, DraftModelTechnique, install_view, load_draft
 
 __all__ = ["PlacedDraftModelConfig", "PlacedDraftModelTechnique", "PlacedDrafter"]
 
@@ -63,6 +63,7 @@ class PlacedDraftModelTechnique(DraftModelTechnique):
         if device.type == "cuda" and (not torch.cuda.is_available() or device.index >= torch.cuda.device_count()):
             raise ConfigError(f"placed_draft_model: device {config.device} is not available")
         self._draft = [load_draft(config, model).to(device)]
+        install_view(self.draft, config)
 
     def drafter(self) -> PlacedDrafter:
         return PlacedDrafter(self.draft, self.model.config.hidden_size, self.model.device)

@@ -237,10 +237,11 @@ class DraftQuantTechnique(_QuantBase):
     """Round-to-nearest quantization of the drafter's projections (lossless: the target verifies every token)."""
 
     config_class = DraftQuantConfig
+    family = Family.DRAFT_COMPRESSION  # quantizes a different model than ``quant``: the two combine
     lossless = True
 
     def conflicts(self, other) -> str | None:
-        return None  # quantizes a different model than ``quant``
+        return None
 
     def _drafter_technique(self):
         return self._drafter

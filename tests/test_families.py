@@ -21,13 +21,30 @@ FAMILIES = {
     "smollm3": dict(no_rope_layers=[1, 0, 1]),
     "olmo2": dict(),
     "qwen3_moe": dict(num_experts=4, num_experts_per_tok=2, moe_intermediate_size=48, norm_topk_prob=False),
+    # GeGLU, (1 + w) norms, dtype-rounded embedding scale, head_dim 16
+    "gemma": dict(head_dim=16),
+    # + sandwich norms, soft-capped scores and logits, sliding window on alternate layers
+    "gemma2": dict(head_dim=16, sliding_window=6, query_pre_attn_scalar=16, attn_logit_softcapping=5.0,
+                   final_logit_softcapping=3.0),
+    # + per-head q/k norms, separate rotary tables for the sliding layers
+    "gemma3_text": dict(head_dim=16, sliding_window=5, query_pre_attn_scalar=24,
+                        layer_types=["sliding_attention", "full_attention", "sliding_attention"],
+                        rope_parameters={"sliding_attention": {"rope_type": "default", "rope_theta": 100.0},
+                                         "full_attention": {"rope_type": "default", "rope_theta": 10000.0}}),
+    "ministral": dict(head_dim=16, sliding_window=7,
+                      layer_types=["sliding_attention", "full_attention", "sliding_attention"]),
+    "olmo3": dict(sliding_window=6, layer_types=["sliding_attention", "sliding_attention", "full_attention"]),
+    "olmoe": dict(num_experts=4, num_experts_per_tok=2, norm_topk_prob=False),
+    "qwen2_moe": dict(num_experts=4, num_experts_per_tok=2, moe_intermediate_size=48,
+                      shared_expert_intermediate_size=40, norm_topk_prob=False),
 }
 
 
 def _hf(name, seed=0):
     cfg = transformers.CONFIG_MAPPING[name](**{**BASE, **FAMILIES[name]})
     torch.manual_seed(seed)
-    model = transformers.AutoModelForCausalLM.from_config(cfg).float().eval()
+    # eager: the reference attention (sdpa drops Gemma-2's score soft-cap)
+    model = transformers.AutoModelForCausalLM.from_config(cfg, attn_implementation="eager").float().eval()
     with torch.no_grad():  # larger than HF's 0.02 init, so the families' differences show in the logits
         for n, p in model.named_parameters():
             if p.dim() >= 2:

@@ -20,6 +20,20 @@ FAMILIES = {
     "smollm3": dict(no_rope_layers=[1, 0, 1]),
     "olmo2": dict(),
     "qwen3_moe": dict(num_experts=8, num_experts_per_tok=2, moe_intermediate_size=256, norm_topk_prob=False),
+    # head dimension 256 (the attention kernel's one-stage layout), GeGLU, (1 + w) norms
+    "gemma": dict(head_dim=256, num_attention_heads=4, num_key_value_heads=1),
+    # soft-capped scores and logits, sandwich norms, sliding windows on alternate layers
+    "gemma2": dict(head_dim=128, sliding_window=80, query_pre_attn_scalar=128, attn_logit_softcapping=20.0,
+                   final_logit_softcapping=15.0),
+    "gemma3_text": dict(head_dim=256, num_attention_heads=4, num_key_value_heads=2, sliding_window=96,
+                        query_pre_attn_scalar=256,
+                        layer_types=["sliding_attention", "full_attention", "sliding_attention"]),
+    "ministral": dict(head_dim=64, sliding_window=70,
+                      layer_types=["sliding_attention", "full_attention", "sliding_attention"]),
+    "olmo3": dict(sliding_window=90, layer_types=["sliding_attention", "sliding_attention", "full_attention"]),
+    "olmoe": dict(num_experts=8, num_experts_per_tok=2, norm_topk_prob=False, intermediate_size=256),
+    "qwen2_moe": dict(num_experts=8, num_experts_per_tok=2, moe_intermediate_size=256,
+                      shared_expert_intermediate_size=384, norm_topk_prob=False),
 }
 
 
@@ -27,16 +41,17 @@ FAMILIES = {
 def test_family_on_gpu(cuda, name):
     cfg = transformers.CONFIG_MAPPING[name](**{**BASE, **FAMILIES[name]})
     torch.manual_seed(0)
-    hf = transformers.AutoModelForCausalLM.from_config(cfg).float().eval()
+    hf = transformers.AutoModelForCausalLM.from_config(cfg, attn_implementation="eager").float().eval()
     cpu = CausalLM.from_hf(hf)
     gpu = CausalLM.from_hf(hf, dtype=torch.bfloat16, device=cuda)
-    ids = torch.randint(1, 1024, (1, 40), generator=torch.Generator().manual_seed(1))
+    ids = torch.randint(1, 1024, (1, 160), generator=torch.Generator().manual_seed(1))  # longer than the windows
     want = eco.apply(cpu)(ids).float()
     got = eco.apply(gpu)(ids.to(cuda)).float().cpu()
     err = (got - want).abs().max().item()
     assert err <= 0.05 * want.abs().max().item() + 0.02, err
     em = eco.apply(gpu, Eagle3Config())
     prompts = [ids[0].to(cuda), ids[0, :17].to(cuda)]
+    eco.ops.attention_usage(reset=True)
     plain = em.decode_batch(prompts, 20, decoding=eco.DecodeConfig(cycle_length=1))
     tree = em.decode_batch(prompts, 20, decoding=eco.DecodeConfig(
         cycle_length=7, draft_policy="dynamic_tree", draft_policy_options={"depth": 6, "topk": 10, "total_tokens": 60},
@@ -44,3 +59,5 @@ def test_family_on_gpu(cuda, name):
     for a, b in zip(plain, tree):
         assert torch.equal(a.tokens, b.tokens)
     assert eco.ops.require().status(0) == 0
+    if gpu.config.sliding_window:  # the windowed layers ran the kernel's window path
+        assert any("window" in mode for (_, _, _, mode) in eco.ops.attention_usage())

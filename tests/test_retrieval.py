@@ -51,3 +51,44 @@ def test_suffix_global_index():
     eff.techniques["suffix_decoding"].add_corpus([torch.cat([p, ref]).tolist()])
     out = eff.decode(p, 12)
     assert torch.equal(out.tokens, ref) and out.mean_accepted > 1.0
+
+
+def test_jacobi_window_fills_and_makes_ngrams():
+    from economize_b200.techniques.lookahead import JacobiWindow
+
+    w = JacobiWindow([10, 11, 12, 13, 14], depth=3)  # W + N - 3 = 5 tokens: W = 4, N = 4
+    toks, pars, last = w.nodes(0)
+    assert toks == [10, 11, 12, 13, 14] and pars == [-1, 0, 1, 2, 3] and last == [0, 1, 2, 3, 4]
+    assert w.step([20, 21, 22, 23, 24], root=1) == []
+    toks, pars, last = w.nodes(2)  # after two verification-branch nodes
+    assert toks == [11, 12, 13, 14, 20, 21, 22, 23, 24]
+    # level 1 column j below the first block's column j: the root, then level 0's tokens
+    assert pars == [-1, 2, 3, 4, -1, 2, 3, 4, 5] and last == [6, 7, 8, 9, 10]
+    assert w.step([30, 31, 32, 33, 34], root=2) == []
+    assert w.full and [len(lv) for lv in w.levels] == [3, 4, 4]  # W - 1, W, W
+    grams = w.step([40, 41, 42, 43], root=3)
+    # one N-gram per column: the first block's column j, then the column down the levels, then the prediction
+    assert grams == [(3, (21, 31, 40)), (12, (22, 32, 41)), (13, (23, 33, 42)), (14, (24, 34, 43))]
+    assert [len(lv) for lv in w.levels] == [3, 4, 4]
+
+
+def test_lookahead_pool_learns_from_the_window_and_accepts():
+    """A model whose greedy output repeats: the Jacobi window converges on the cycle, its n-grams reach the pool and
+    the verification branch accepts them; the output equals plain greedy decoding."""
+    model = tiny_model()
+    p = _repetitive_prompt()
+    ref = reference_greedy(model, p, 40)
+    eff = eco.apply(model, LookaheadConfig(window=5, ngram=4, guesses=5))
+    out = eff.decode(p, 40)
+    assert torch.equal(out.tokens, ref)
+    assert out.mean_accepted > 1.2  # n-grams from the window are accepted
+    assert eff.techniques["lookahead"].config.budget <= 63
+
+
+def test_lookahead_refuses_trees_beyond_the_pass():
+    import pytest
+
+    from economize_b200.errors import ConfigError
+
+    with pytest.raises(ConfigError, match="nodes"):
+        LookaheadConfig(window=15, ngram=5, guesses=15)
