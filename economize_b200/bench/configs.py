@@ -95,8 +95,9 @@ def config3(scale: str = "full", device: str | torch.device = "cuda", tp=None, b
     if scale == "full":
         cfg, removed = llama31_70b(), 8
     else:
-        cfg = tiny_llama(hidden_size=256, num_heads=4, num_kv_heads=2, intermediate_size=512, num_layers=10,
-                         vocab_size=1024)
+        # head dimension 128: the fp8 cache kernels' width
+        cfg = tiny_llama(hidden_size=256, num_heads=2, num_kv_heads=1, head_dim=128, intermediate_size=512,
+                         num_layers=10, vocab_size=1024)
         removed = 2
     dtype = torch.bfloat16 if torch.device(device).type == "cuda" else torch.float32
     model = _target(cfg, dtype, device)
@@ -177,7 +178,9 @@ def config5(scale: str = "full", device: str | torch.device = "cuda", draft_devi
         dcfg = llama31_8b(num_layers=16, hidden_size=2048, num_heads=32, num_kv_heads=8, head_dim=64,
                           intermediate_size=8192)
     else:
-        cfg = tiny_llama(num_layers=4, vocab_size=1024, max_position_embeddings=8192)
+        # head dimension 128: the KIVI kernels' width
+        cfg = tiny_llama(num_layers=4, num_heads=2, num_kv_heads=1, head_dim=128, vocab_size=1024,
+                         max_position_embeddings=8192)
         dcfg = tiny_llama(num_layers=2, hidden_size=128, num_heads=2, num_kv_heads=1, head_dim=64,
                           intermediate_size=256, vocab_size=1024, max_position_embeddings=8192)
     draft_device = draft_device or device

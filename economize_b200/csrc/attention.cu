@@ -251,7 +251,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                    const float* __restrict__ k_scale, const float* __restrict__ v_scale,
                    const uint32_t* __restrict__ keep, float* __restrict__ lse_out,
                    const uint8_t* __restrict__ kivi, const int* __restrict__ kivi_chunks, int kivi_bits, int tail_w,
-                   AttnOpts opts) {
+                   AttnOpts opts, KVPages pages) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   static_assert(D == 64 || D == 128 || D == 256, "head dimensions 64, 128 and 256");
@@ -324,10 +324,9 @@ __global__ void __launch_bounds__(kThreads, 1)
   const int c0 = (g0 + split) * chunks_per_split;
   const int c1 = min(n_chunks, c0 + chunks_per_split);
 
-  const size_t kv_row0 = (static_cast<size_t>(b) * Hkv + kvh) * S;
   const int q_chunks = (!FP8 && kivi != nullptr) ? kivi_chunks[b] : 0;  // chunks [0, q_chunks) are KIVI-coded
   auto issue_kv = [&](int c, int s) {
-    const int y = static_cast<int>(kv_row0 + static_cast<size_t>(c) * kKeys);
+    const int y = static_cast<int>(kv_row(pages, b, Hkv, kvh, S, c * kKeys));
     if (c < q_chunks) {  // filled by the threads at its turn; the stage barrier completes without bytes
       mbar_arrive(&kv_full[s]);
       return;
@@ -347,7 +346,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   };
   // kSingle: K and V of chunk c into the single stage, each on its own barrier
   auto issue_one = [&](int c, bool is_v) {
-    const int y = static_cast<int>(kv_row0 + static_cast<size_t>(c) * kKeys);
+    const int y = static_cast<int>(kv_row(pages, b, Hkv, kvh, S, c * kKeys));
     uint64_t* bar = &kv_full[is_v ? 1 : 0];
     uint8_t* dst = is_v ? v_tiles : k_tiles;
     mbar_arrive_expect_tx(bar, kAtoms * kAtom);
@@ -673,7 +672,7 @@ __global__ void __launch_bounds__(128) attn_merge_tail_kernel(
     const uint8_t* __restrict__ k_cache, const uint8_t* __restrict__ v_cache, const int* __restrict__ kv_len,
     const int* __restrict__ n_new, const int64_t* __restrict__ mask, int S, float scale_log2, int q_offset,
     int tail_w, const float* __restrict__ k_scale, const float* __restrict__ v_scale,
-    const uint32_t* __restrict__ keep, float softcap, const float* __restrict__ sinks) {
+    const uint32_t* __restrict__ keep, float softcap, const float* __restrict__ sinks, KVPages pages) {
   __shared__ int s_row[4][kTailKeysMax];    // cache rows of this warp's tail keys, in position order
   __shared__ float s_sc[4][kTailKeysMax];   // their scaled scores
   pdl_trigger();
@@ -697,7 +696,6 @@ __global__ void __launch_bounds__(128) attn_merge_tail_kernel(
   const uint64_t bits = use_mask ? static_cast<uint64_t>(mask[static_cast<size_t>(b) * T + t]) : 0ull;
   const int depth = max(0, use_mask ? (__popcll(bits) - 1) : (q_offset + t));  // a row seeing no new key: 0
   const int lo = max(0, base + depth - tail_w);
-  const size_t row0 = (static_cast<size_t>(b) * Hkv + kvh) * S;
   constexpr int E = D / 32;
   float qv[E];
   load_kv<E>(reinterpret_cast<const uint8_t*>(q), (static_cast<size_t>(b) * T + t) * H + head, lane, false, qv);
@@ -736,7 +734,7 @@ __global__ void __launch_bounds__(128) attn_merge_tail_kernel(
     float kv[kTailBatch][E];
 #pragma unroll
     for (int u = 0; u < kTailBatch; ++u)
-      if (i0 + u < n_keys) load_kv<E>(k_cache, row0 + s_row[wid][i0 + u], lane, fp8, kv[u]);
+      if (i0 + u < n_keys) load_kv<E>(k_cache, kv_row(pages, b, Hkv, kvh, S, s_row[wid][i0 + u]), lane, fp8, kv[u]);
 #pragma unroll
     for (int u = 0; u < kTailBatch; ++u) {
       if (i0 + u < n_keys) {
@@ -767,7 +765,7 @@ __global__ void __launch_bounds__(128) attn_merge_tail_kernel(
     float vv[kTailBatch][E];
 #pragma unroll
     for (int u = 0; u < kTailBatch; ++u)
-      if (i0 + u < n_keys) load_kv<E>(v_cache, row0 + s_row[wid][i0 + u], lane, fp8, vv[u]);
+      if (i0 + u < n_keys) load_kv<E>(v_cache, kv_row(pages, b, Hkv, kvh, S, s_row[wid][i0 + u]), lane, fp8, vv[u]);
 #pragma unroll
     for (int u = 0; u < kTailBatch; ++u) {
       if (i0 + u < n_keys) {
@@ -800,7 +798,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     attn_scores_kernel(const bf16* __restrict__ q, const __grid_constant__ CUtensorMap tm_k,
                        const float* __restrict__ lse2, float* __restrict__ scores, const int* __restrict__ kv_len,
                        const int* __restrict__ n_new, const int64_t* __restrict__ mask, int T, int H, int Hkv, int S,
-                       float scale_log2, int q_offset, int m_tiles, unsigned* status) {
+                       float scale_log2, int q_offset, int m_tiles, unsigned* status, KVPages pages) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* q_tile = smem;
@@ -836,7 +834,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     *abort_flag = 0;
     fence_mbar_init();
     mbar_arrive_expect_tx(kv_full, 2 * kAtom);
-    const int y = static_cast<int>((static_cast<size_t>(b) * Hkv + kvh) * S + static_cast<size_t>(c) * kKeys);
+    const int y = static_cast<int>(kv_row(pages, b, Hkv, kvh, S, c * kKeys));
     tma_load_2d(k_tile, &tm_k, kv_full, 0, y);
     tma_load_2d(k_tile + kAtom, &tm_k, kv_full, 64, y);
   }
@@ -902,7 +900,7 @@ __global__ void __launch_bounds__(kThreads, 1)
 __global__ void __launch_bounds__(128) kivi_quantize_kernel(const bf16* __restrict__ cache, uint8_t* __restrict__ kivi,
                                                             const int* __restrict__ kv_len,
                                                             const int* __restrict__ chunks, int B, int Hkv, int S,
-                                                            int bits, int residual) {
+                                                            int bits, int residual, KVLayout layout) {
   pdl_trigger();
   pdl_wait();
   const int layer = blockIdx.x, bh = blockIdx.y, b = bh / Hkv;
@@ -911,9 +909,9 @@ __global__ void __launch_bounds__(128) kivi_quantize_kernel(const bf16* __restri
   __shared__ uint8_t codes[kKeys][kDim + 4];
   const int tid = threadIdx.x;
   const float levels = static_cast<float>((1 << bits) - 1);
-  const size_t plane = static_cast<size_t>(B) * Hkv * S * kDim;  // one of K / V of one layer
-  const bf16* K = cache + (static_cast<size_t>(layer) * 2) * plane + (static_cast<size_t>(bh) * S + c * kKeys) * kDim;
-  const bf16* V = K + plane;
+  const int kvh = bh % Hkv;
+  const bf16* K = cache + kv_layer_row(layout, layer, 0, b, Hkv, kvh, S, c * kKeys) * kDim;
+  const bf16* V = cache + kv_layer_row(layout, layer, 1, b, Hkv, kvh, S, c * kKeys) * kDim;
   uint8_t* out = kivi + ((static_cast<size_t>(layer) * B * Hkv + bh) * (S / kKeys) + c) * kivi_chunk_bytes(bits);
   bf16* ks = reinterpret_cast<bf16*>(out + kivi_code_bytes(bits));
   bf16* kz = ks + kDim;
@@ -1014,7 +1012,7 @@ int launch_attention(const void* q, const CUtensorMap* tm_k, const CUtensorMap* 
                      int S, float scale, int q_offset, const AttnPlan& plan, unsigned* status, cudaStream_t stream,
                      unsigned long long* trace, const float* k_scale, const float* v_scale, const uint32_t* keep,
                      float* lse_out, const uint8_t* kivi, const int* kivi_chunks, int kivi_bits, int tail_w,
-                     const void* k_cache, const void* v_cache, const AttnOpts& opts) {
+                     const void* k_cache, const void* v_cache, const AttnOpts& opts, const KVPages& pages) {
   if (kivi != nullptr && (k_scale != nullptr || (kivi_bits != 2 && kivi_bits != 4))) return -1;
   if (tail_w < 0 || tail_w > 64 || (tail_w > 0 && (!plan.tail || k_cache == nullptr || v_cache == nullptr)))
     return -1;
@@ -1038,7 +1036,7 @@ int launch_attention(const void* q, const CUtensorMap* tm_k, const CUtensorMap* 
     launch_pdl(kernel, grid, dim3(kThreads), smem, stream, static_cast<const bf16*>(q), *tm_k, *tm_v,
                static_cast<bf16*>(out), ws_o, ws_ml, kv_len, n_new, mask, T, H, Hkv, S, sl2, q_offset,
                plan.chunks_per_split, plan.m_tiles, status, trace, k_scale, v_scale, keep, lse_out, kivi, kivi_chunks,
-               kivi_bits, tail_w, opts);
+               kivi_bits, tail_w, opts, pages);
   };
   if (D == 64) run(attn_tc_kernel<false, 64>, attn_smem_bytes(64));
   else if (D == 256) run(attn_tc_kernel<false, 256>, attn_smem_bytes(256));
@@ -1052,7 +1050,7 @@ int launch_attention(const void* q, const CUtensorMap* tm_k, const CUtensorMap* 
                static_cast<const float*>(ws_ml), static_cast<bf16*>(out), T, H, Hkv, plan.m_tiles, plan.splits,
                lse_out, static_cast<const bf16*>(q), static_cast<const uint8_t*>(k_cache),
                static_cast<const uint8_t*>(v_cache), kv_len, n_new, mask, S, sl2, q_offset, tail_w, k_scale, v_scale,
-               keep, opts.softcap, opts.sinks);
+               keep, opts.softcap, opts.sinks, pages);
   } else if (plan.splits > 1) {
     auto merge = D == 64 ? attn_merge_kernel<64> : D == 256 ? attn_merge_kernel<256> : attn_merge_kernel<128>;
     launch_pdl(merge, mgrid, dim3(128), 0, stream, static_cast<const float*>(ws_o),
@@ -1064,25 +1062,27 @@ int launch_attention(const void* q, const CUtensorMap* tm_k, const CUtensorMap* 
 
 int launch_attention_scores(const void* q, const CUtensorMap* tm_k, const float* lse2, float* scores,
                             const int* kv_len, const int* n_new, const int64_t* mask, int B, int T, int H, int Hkv,
-                            int D, int S, float scale, int q_offset, unsigned* status, cudaStream_t stream) {
+                            int D, int S, float scale, int q_offset, unsigned* status, cudaStream_t stream,
+                            const KVPages& pages) {
   if (D != kDim || H % Hkv != 0 || (mask != nullptr && T > 64)) return -1;
   set_max_smem(attn_scores_kernel, kScoreSmem);
   const int G = H / Hkv;
   const int m_tiles = (T * G + kRows - 1) / kRows;
   dim3 grid(B * Hkv * m_tiles, (S + kKeys - 1) / kKeys);
   launch_pdl(attn_scores_kernel, grid, dim3(kThreads), kScoreSmem, stream, static_cast<const bf16*>(q), *tm_k, lse2,
-             scores, kv_len, n_new, mask, T, H, Hkv, S, scale * 1.4426950408889634f, q_offset, m_tiles, status);
+             scores, kv_len, n_new, mask, T, H, Hkv, S, scale * 1.4426950408889634f, q_offset, m_tiles, status,
+             pages);
   return 0;
 }
 
 int kivi_chunk_size(int bits) { return kivi_chunk_bytes(bits); }
 
 int launch_kivi_quantize(const void* cache, void* kivi, const int* kv_len, int* chunks, int L, int B, int Hkv, int S,
-                         int D, int bits, int residual, int max_new, cudaStream_t stream) {
+                         int D, int bits, int residual, int max_new, cudaStream_t stream, const KVLayout& layout) {
   if (D != kDim || S % kKeys != 0 || (bits != 2 && bits != 4) || max_new < 1) return -1;
   launch_pdl(kivi_quantize_kernel, dim3(L, B * Hkv, max_new), dim3(kKeys), 0, stream,
              static_cast<const bf16*>(cache), static_cast<uint8_t*>(kivi), kv_len, static_cast<const int*>(chunks), B,
-             Hkv, S, bits, residual);
+             Hkv, S, bits, residual, layout);
   launch_pdl(kivi_advance_kernel, dim3((B + 127) / 128), dim3(128), 0, stream, kv_len, chunks, B, max_new, residual);
   return 0;
 }

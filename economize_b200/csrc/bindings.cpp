@@ -181,10 +181,84 @@ bool fp8_cache(const Tensor& k_cache, const c10::optional<Tensor>& k_scale, cons
   return true;
 }
 
+// One layer's K or V cache argument: a contiguous [B, Hkv, S, D] tensor, or, with a page table [B, C] (int32), a view
+// [P, Hkv, 128, D] of a page pool whose pages start stride(0) elements apart (dims 1-3 packed). Gives the logical
+// capacity S, the kernels' page description and the rows a 2-D TMA map over the view may address.
+struct CacheArg {
+  int S = 0;
+  uint64_t rows = 0;
+  ecz::KVPages pages;
+};
+
+CacheArg cache_arg(const Tensor& cache, const c10::optional<Tensor>& table, int64_t B, const char* what) {
+  TORCH_CHECK(cache.dim() == 4, what, ": caches must be 4-D ([B, Hkv, S, D], or page-pool views [P, Hkv, 128, D])");
+  const int64_t Hkv = cache.size(1), D = cache.size(3);
+  CacheArg a;
+  if (!table.has_value()) {
+    TORCH_CHECK(cache.is_contiguous(), what, ": caches must be contiguous");
+    a.S = static_cast<int>(cache.size(2));
+    a.rows = static_cast<uint64_t>(cache.size(0)) * Hkv * a.S;
+    return a;
+  }
+  CHECK_I32(*table);
+  CHECK_ON(*table, cache);
+  TORCH_CHECK(table->dim() == 2 && table->size(0) == B && table->is_contiguous(), what,
+              ": page tables must be contiguous int32 [B, chunks]");
+  TORCH_CHECK(cache.size(2) == 128 && cache.stride(3) == 1 && cache.stride(2) == D && cache.stride(1) == 128 * D &&
+                  cache.stride(0) % (128 * D) == 0 && cache.stride(0) >= Hkv * 128 * D,
+              what, ": a paged cache must be a view [P, Hkv, 128, D] of whole pages");
+  a.S = static_cast<int>(table->size(1) * 128);
+  a.pages.table = table->data_ptr<int>();
+  a.pages.max_chunks = static_cast<int>(table->size(1));
+  a.pages.page_rows = static_cast<int>(cache.stride(0) / D);
+  a.rows = static_cast<uint64_t>(cache.size(0) - 1) * a.pages.page_rows + static_cast<uint64_t>(Hkv) * 128;
+  return a;
+}
+
+// A whole cache (every layer): contiguous [L, 2, B, Hkv, S, D], or a page pool [P, 2, Hkv, 128, D] with page tables
+// [L, B, C] (int32).
+struct WholeCache {
+  int L = 0, B = 0, Hkv = 0, S = 0, D = 0;
+  ecz::KVLayout layout;
+};
+
+WholeCache whole_cache(const Tensor& cache, const c10::optional<Tensor>& tables, const char* what) {
+  TORCH_CHECK(cache.is_contiguous(), what, ": the cache must be contiguous");
+  WholeCache w;
+  if (!tables.has_value()) {
+    TORCH_CHECK(cache.dim() == 6, what, ": the cache must be [L, 2, B, Hkv, S, D]");
+    w.L = static_cast<int>(cache.size(0));
+    w.B = static_cast<int>(cache.size(2));
+    w.Hkv = static_cast<int>(cache.size(3));
+    w.S = static_cast<int>(cache.size(4));
+    w.D = static_cast<int>(cache.size(5));
+    w.layout.v_rows = static_cast<long>(w.B) * w.Hkv * w.S;
+    w.layout.layer_rows = 2 * w.layout.v_rows;
+    return w;
+  }
+  CHECK_I32(*tables);
+  CHECK_ON(*tables, cache);
+  TORCH_CHECK(cache.dim() == 5 && cache.size(1) == 2 && cache.size(3) == 128, what,
+              ": a paged cache must be a pool [P, 2, Hkv, 128, D]");
+  TORCH_CHECK(tables->dim() == 3 && tables->is_contiguous(), what, ": page tables must be int32 [L, B, chunks]");
+  w.L = static_cast<int>(tables->size(0));
+  w.B = static_cast<int>(tables->size(1));
+  w.Hkv = static_cast<int>(cache.size(2));
+  w.S = static_cast<int>(tables->size(2) * 128);
+  w.D = static_cast<int>(cache.size(4));
+  w.layout.pages.table = tables->data_ptr<int>();
+  w.layout.pages.max_chunks = static_cast<int>(tables->size(2));
+  w.layout.pages.page_rows = 2 * w.Hkv * 128;
+  w.layout.table_stride = static_cast<long>(w.B) * tables->size(2);
+  w.layout.layer_rows = 0;
+  w.layout.v_rows = static_cast<long>(w.Hkv) * 128;
+  return w;
+}
+
 Tensor rope_store(Tensor qkv, Tensor positions, Tensor cos, Tensor sin, int64_t H, int64_t Hkv, int64_t D,
                   Tensor k_cache, Tensor v_cache, Tensor kv_len, Tensor n_new, c10::optional<Tensor> q_norm,
                   c10::optional<Tensor> k_norm, double eps, int64_t q_offset, c10::optional<Tensor> k_scale,
-                  c10::optional<Tensor> v_scale) {
+                  c10::optional<Tensor> v_scale, c10::optional<Tensor> pages) {
   CHECK_CUDA(qkv);
   TORCH_CHECK(D == 64 || D == 128 || D == 256, "rope_store: head_dim must be 64, 128 or 256, got ", D);
   const auto [qkv_splits, qkv_shape] = parts_of(qkv);
@@ -201,12 +275,16 @@ Tensor rope_store(Tensor qkv, Tensor positions, Tensor cos, Tensor sin, int64_t 
   CHECK_ON(k_cache, qkv);
   CHECK_ON(v_cache, qkv);
   TORCH_CHECK(cos.scalar_type() == at::kFloat && sin.scalar_type() == at::kFloat, "rope tables must be fp32");
-  TORCH_CHECK(k_cache.dim() == 4, "rope_store expects caches [B, Hkv, S, D]");
-  TORCH_CHECK(k_cache.is_contiguous() && v_cache.is_contiguous(), "caches must be contiguous");
+  TORCH_CHECK(cos.dim() == 2 && cos.size(1) == D / 2 && sin.sizes() == cos.sizes() && cos.is_contiguous() &&
+                  sin.is_contiguous(), "rope tables must be contiguous fp32 [positions, D / 2]");
   c10::cuda::CUDAGuard guard(qkv.device());
   if (!qkv_splits) qkv = qkv.contiguous();
   positions = positions.contiguous();
   const int B = static_cast<int>(qkv_shape[0]), T = static_cast<int>(qkv_shape[1]);
+  const CacheArg ca = cache_arg(k_cache, pages, B, "rope_store");
+  const CacheArg cv = cache_arg(v_cache, pages, B, "rope_store");
+  TORCH_CHECK(ca.pages.page_rows == cv.pages.page_rows && k_cache.sizes() == v_cache.sizes(),
+              "rope_store: K and V caches must share a layout");
   TORCH_CHECK(qkv_shape.size() == 3 && qkv_shape[2] == (H + 2 * Hkv) * D, "qkv width mismatch");
   auto q = at::empty({B, T, H, D}, qkv.options().dtype(at::kBFloat16));
   const int rc = ecz::launch_rope_store(
@@ -214,9 +292,10 @@ Tensor rope_store(Tensor qkv, Tensor positions, Tensor cos, Tensor sin, int64_t 
       k_cache.data_ptr(), v_cache.data_ptr(), kv_len.data_ptr<int>(), n_new.data_ptr<int>(),
       q_norm.has_value() ? q_norm->data_ptr() : nullptr, k_norm.has_value() ? k_norm->data_ptr() : nullptr,
       static_cast<float>(eps), B, T, static_cast<int>(H), static_cast<int>(Hkv), static_cast<int>(D),
-      static_cast<int>(k_cache.size(2)), static_cast<int>(q_offset), at::cuda::getCurrentCUDAStream(),
+      ca.S, static_cast<int>(q_offset), at::cuda::getCurrentCUDAStream(),
       fp8 ? k_scale->data_ptr<float>() : nullptr, fp8 ? v_scale->data_ptr<float>() : nullptr,
-      qkv_splits ? qkv.data_ptr<float>() : nullptr, qkv_splits);
+      qkv_splits ? qkv.data_ptr<float>() : nullptr, qkv_splits, ca.pages, static_cast<int>(cos.size(0)),
+      status_word(qkv.device()));
   TORCH_CHECK(rc == 0, "rope_store: unsupported head_dim ", D);
   return q;
 }
@@ -225,7 +304,7 @@ Tensor attention(Tensor q, Tensor k_cache, Tensor v_cache, Tensor kv_len, Tensor
                  double scale, int64_t q_offset, c10::optional<Tensor> trace, c10::optional<Tensor> k_scale,
                  c10::optional<Tensor> v_scale, c10::optional<Tensor> keep, c10::optional<Tensor> lse_out,
                  c10::optional<Tensor> kivi, c10::optional<Tensor> kivi_chunks, int64_t kivi_bits, int64_t tail,
-                 double softcap, c10::optional<Tensor> sinks, int64_t window) {
+                 double softcap, c10::optional<Tensor> sinks, int64_t window, c10::optional<Tensor> pages) {
   CHECK_CUDA(q);
   CHECK_BF16(q);
   TORCH_CHECK(q.dim() == 4 && (q.size(3) == 128 || q.size(3) == 64 || q.size(3) == 256) && k_cache.dim() == 4,
@@ -256,12 +335,16 @@ Tensor attention(Tensor q, Tensor k_cache, Tensor v_cache, Tensor kv_len, Tensor
   if (kivi.has_value()) CHECK_ON(*kivi, q);
   if (kivi_chunks.has_value()) CHECK_ON(*kivi_chunks, q);
   TORCH_CHECK(q.dim() == 4 && k_cache.dim() == 4, "attention expects q [B, T, H, D] and caches [B, Hkv, S, D]");
-  TORCH_CHECK(k_cache.is_contiguous() && v_cache.is_contiguous(), "caches must be contiguous");
   c10::cuda::CUDAGuard guard(q.device());
   q = q.contiguous();
   const int B = static_cast<int>(q.size(0)), T = static_cast<int>(q.size(1)), H = static_cast<int>(q.size(2)),
             D = static_cast<int>(q.size(3));
-  const int Hkv = static_cast<int>(k_cache.size(1)), S = static_cast<int>(k_cache.size(2));
+  const CacheArg ck = cache_arg(k_cache, pages, B, "attention");
+  const CacheArg cv = cache_arg(v_cache, pages, B, "attention");
+  TORCH_CHECK(ck.pages.page_rows == cv.pages.page_rows && k_cache.sizes() == v_cache.sizes(),
+              "attention: K and V caches must share a layout");
+  if (!pages.has_value()) TORCH_CHECK(k_cache.size(0) == B, "attention: caches must have q's batch");
+  const int Hkv = static_cast<int>(k_cache.size(1)), S = ck.S;
   const int64_t* mask_ptr = nullptr;
   Tensor m;
   if (mask.has_value()) {
@@ -298,11 +381,10 @@ Tensor attention(Tensor q, Tensor k_cache, Tensor v_cache, Tensor kv_len, Tensor
   opts.window = static_cast<int>(window);
   Tensor ws;
   if (plan.ws_floats > 0) ws = at::empty({plan.ws_floats}, q.options().dtype(at::kFloat));
-  const uint64_t rows = static_cast<uint64_t>(B) * Hkv * S;
-  const CUtensorMap* tk = fp8 ? tensor_map_ex(k_cache.data_ptr(), 1, rows, D, D, D, 128, 0)
-                              : tensor_map(k_cache.data_ptr(), rows, D, D, 128);
-  const CUtensorMap* tv = fp8 ? tensor_map_ex(v_cache.data_ptr(), 1, rows, D, D, D, 128, 0)
-                              : tensor_map(v_cache.data_ptr(), rows, D, D, 128);
+  const CUtensorMap* tk = fp8 ? tensor_map_ex(k_cache.data_ptr(), 1, ck.rows, D, D, D, 128, 0)
+                              : tensor_map(k_cache.data_ptr(), ck.rows, D, D, 128);
+  const CUtensorMap* tv = fp8 ? tensor_map_ex(v_cache.data_ptr(), 1, cv.rows, D, D, D, 128, 0)
+                              : tensor_map(v_cache.data_ptr(), cv.rows, D, D, 128);
   cudaStream_t stream = at::cuda::getCurrentCUDAStream();
   const int rc = ecz::launch_attention(q.data_ptr(), tk, tv, out.data_ptr(),
                                        plan.ws_floats > 0 ? ws.data_ptr<float>() : nullptr, kv_len.data_ptr<int>(),
@@ -320,7 +402,7 @@ Tensor attention(Tensor q, Tensor k_cache, Tensor v_cache, Tensor kv_len, Tensor
                                        kivi.has_value() ? kivi->data_ptr<uint8_t>() : nullptr,
                                        kivi.has_value() ? kivi_chunks->data_ptr<int>() : nullptr,
                                        static_cast<int>(kivi_bits), static_cast<int>(tail), k_cache.data_ptr(),
-                                       v_cache.data_ptr(), opts);
+                                       v_cache.data_ptr(), opts, ck.pages);
   TORCH_CHECK(rc == 0, "attention: unsupported shape (head_dim 64, 128 or 256, fp8 and KIVI caches at 128, H "
               "divisible by H_kv)");
   return out;
@@ -623,7 +705,7 @@ Tensor linear_sp24(Tensor x, Tensor values, Tensor meta, int64_t splits) {
 // Accumulate KV-eviction scores [B, Hkv, S] (fp32, in place) for the queries q [B, T, H, D] of a pass whose
 // log2-domain log-sum-exp lse2 [B, T, H] came from attention(..., lse_out=).
 void attention_scores(Tensor q, Tensor k_cache, Tensor kv_len, Tensor n_new, c10::optional<Tensor> mask,
-                      Tensor lse2, Tensor scores, double scale, int64_t q_offset) {
+                      Tensor lse2, Tensor scores, double scale, int64_t q_offset, c10::optional<Tensor> pages) {
   CHECK_CUDA(q);
   CHECK_BF16(q);
   CHECK_BF16(k_cache);
@@ -631,7 +713,8 @@ void attention_scores(Tensor q, Tensor k_cache, Tensor kv_len, Tensor n_new, c10
   c10::cuda::CUDAGuard guard(q.device());
   q = q.contiguous();
   const int B = static_cast<int>(q.size(0)), T = static_cast<int>(q.size(1)), H = static_cast<int>(q.size(2));
-  const int Hkv = static_cast<int>(k_cache.size(1)), S = static_cast<int>(k_cache.size(2));
+  const CacheArg ck = cache_arg(k_cache, pages, B, "attention_scores");
+  const int Hkv = static_cast<int>(k_cache.size(1)), S = ck.S;
   TORCH_CHECK(scores.scalar_type() == at::kFloat && scores.is_contiguous() &&
                   scores.numel() == static_cast<int64_t>(B) * Hkv * S, "scores must be fp32 [B, Hkv, S]");
   TORCH_CHECK(lse2.scalar_type() == at::kFloat && lse2.numel() == static_cast<int64_t>(B) * T * H, "lse2 [B, T, H]");
@@ -646,17 +729,17 @@ void attention_scores(Tensor q, Tensor k_cache, Tensor kv_len, Tensor n_new, c10
     m = mask->contiguous();
     CHECK_I64(m);
   }
-  const CUtensorMap* tk = tensor_map(k_cache.data_ptr(), static_cast<uint64_t>(B) * Hkv * S, 128, 128, 128);
+  const CUtensorMap* tk = tensor_map(k_cache.data_ptr(), ck.rows, 128, 128, 128);
   const int rc = ecz::launch_attention_scores(q.data_ptr(), tk, lse2.contiguous().data_ptr<float>(),
                                               scores.data_ptr<float>(), kv_len.data_ptr<int>(), n_new.data_ptr<int>(),
                                               mask.has_value() ? m.data_ptr<int64_t>() : nullptr, B, T, H, Hkv, 128, S,
                                               static_cast<float>(scale), static_cast<int>(q_offset),
-                                              status_word(q.device()), at::cuda::getCurrentCUDAStream());
+                                              status_word(q.device()), at::cuda::getCurrentCUDAStream(), ck.pages);
   TORCH_CHECK(rc == 0, "attention_scores: unsupported shape");
 }
 
 void kivi_quantize(Tensor cache, Tensor kivi, Tensor kv_len, Tensor chunks, int64_t bits, int64_t residual,
-                   int64_t max_new) {
+                   int64_t max_new, c10::optional<Tensor> pages) {
   CHECK_CUDA(cache);
   CHECK_BF16(cache);
   CHECK_I32(kv_len);
@@ -665,17 +748,16 @@ void kivi_quantize(Tensor cache, Tensor kivi, Tensor kv_len, Tensor chunks, int6
   CHECK_ON(kivi, cache);
   CHECK_ON(kv_len, cache);
   CHECK_ON(chunks, cache);
-  TORCH_CHECK(cache.dim() == 6 && cache.is_contiguous(), "cache must be a contiguous [L, 2, B, Hkv, S, D] tensor");
+  const WholeCache w = whole_cache(cache, pages, "kivi_quantize");
   c10::cuda::CUDAGuard guard(cache.device());
-  const int L = static_cast<int>(cache.size(0)), B = static_cast<int>(cache.size(2)), Hkv = static_cast<int>(cache.size(3));
-  const int S = static_cast<int>(cache.size(4)), D = static_cast<int>(cache.size(5));
+  const int L = w.L, B = w.B, Hkv = w.Hkv, S = w.S, D = w.D;
   TORCH_CHECK(kivi.scalar_type() == at::kByte && kivi.is_contiguous() &&
                   kivi.numel() == static_cast<int64_t>(L) * B * Hkv * (S / 128) * ecz::kivi_chunk_size(bits),
               "kivi storage must be [L, B, Hkv, S / 128, chunk bytes]");
   const int rc = ecz::launch_kivi_quantize(cache.data_ptr(), kivi.data_ptr(), kv_len.data_ptr<int>(),
                                            chunks.data_ptr<int>(), L, B, Hkv, S, D, static_cast<int>(bits),
                                            static_cast<int>(residual), static_cast<int>(max_new),
-                                           at::cuda::getCurrentCUDAStream());
+                                           at::cuda::getCurrentCUDAStream(), w.layout);
   TORCH_CHECK(rc == 0, "kivi_quantize: head_dim 128, 2 or 4 bits");
 }
 
@@ -773,7 +855,7 @@ std::tuple<Tensor, Tensor, Tensor> greedy_accept(Tensor tokens, Tensor parents, 
   return {n_acc, path, out};
 }
 
-void kv_compact(Tensor cache, Tensor kv_len, Tensor path, Tensor n_acc) {
+void kv_compact(Tensor cache, Tensor kv_len, Tensor path, Tensor n_acc, c10::optional<Tensor> pages) {
   CHECK_CUDA(cache);
   TORCH_CHECK(cache.element_size() == 2 || cache.element_size() == 1, "cache must be bf16 or fp8");
   CHECK_I32(kv_len);
@@ -782,18 +864,15 @@ void kv_compact(Tensor cache, Tensor kv_len, Tensor path, Tensor n_acc) {
   CHECK_ON(kv_len, cache);
   CHECK_ON(path, cache);
   CHECK_ON(n_acc, cache);
-  TORCH_CHECK(cache.dim() == 6 && cache.is_contiguous(), "cache must be a contiguous [L, 2, B, Hkv, S, D] tensor");
+  const WholeCache w = whole_cache(cache, pages, "kv_compact");
   c10::cuda::CUDAGuard guard(cache.device());
   path = path.contiguous();
-  const int LH = static_cast<int>(cache.size(0) * cache.size(1));
-  const int B = static_cast<int>(cache.size(2)), Hkv = static_cast<int>(cache.size(3));
-  const int S = static_cast<int>(cache.size(4)), D = static_cast<int>(cache.size(5));
   const int T = static_cast<int>(path.size(1));
   const int max_depth = std::max(1, T - 1);
   const int rc = ecz::launch_kv_compact(cache.data_ptr(), kv_len.data_ptr<int>(), path.data_ptr<int>(),
-                                        n_acc.data_ptr<int>(), LH, B, Hkv, S, D * static_cast<int>(cache.element_size()),
-                                        T, std::min(max_depth, 64),
-                                        at::cuda::getCurrentCUDAStream());
+                                        n_acc.data_ptr<int>(), w.L, w.B, w.Hkv, w.S,
+                                        w.D * static_cast<int>(cache.element_size()), T, std::min(max_depth, 64),
+                                        at::cuda::getCurrentCUDAStream(), w.layout);
   TORCH_CHECK(rc == 0, "kv_compact: unsupported head_dim or path length");
 }
 
@@ -1341,16 +1420,21 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
         py::arg("qkv"), py::arg("positions"), py::arg("cos"), py::arg("sin"), py::arg("H"), py::arg("Hkv"),
         py::arg("D"), py::arg("k_cache"), py::arg("v_cache"), py::arg("kv_len"), py::arg("n_new"), py::arg("q_norm"),
         py::arg("k_norm"), py::arg("eps"), py::arg("q_offset"), py::arg("k_scale") = py::none(),
-        py::arg("v_scale") = py::none());
+        py::arg("v_scale") = py::none(), py::arg("pages") = py::none());
   m.def("attention", &attention, "tree-masked / causal attention over the slot cache (tcgen05; bf16 or fp8 KV)",
         py::arg("q"), py::arg("k_cache"), py::arg("v_cache"), py::arg("kv_len"), py::arg("n_new"), py::arg("mask"),
         py::arg("scale"), py::arg("q_offset"), py::arg("trace") = py::none(), py::arg("k_scale") = py::none(),
         py::arg("v_scale") = py::none(), py::arg("keep") = py::none(), py::arg("lse_out") = py::none(),
         py::arg("kivi") = py::none(), py::arg("kivi_chunks") = py::none(), py::arg("kivi_bits") = 0,
-        py::arg("tail") = 0, py::arg("softcap") = 0.0, py::arg("sinks") = py::none(), py::arg("window") = 0);
+        py::arg("tail") = 0, py::arg("softcap") = 0.0, py::arg("sinks") = py::none(), py::arg("window") = 0,
+        py::arg("pages") = py::none());
   m.def("kivi_chunk_size", &ecz::kivi_chunk_size, "bytes of one KIVI-coded 128-key chunk");
-  m.def("kivi_quantize", &kivi_quantize, "quantise committed cache chunks to KIVI codes and advance the counts");
-  m.def("attention_scores", &attention_scores, "accumulate KV-eviction attention scores (tcgen05)");
+  m.def("kivi_quantize", &kivi_quantize, "quantise committed cache chunks to KIVI codes and advance the counts",
+        py::arg("cache"), py::arg("kivi"), py::arg("kv_len"), py::arg("chunks"), py::arg("bits"), py::arg("residual"),
+        py::arg("max_new"), py::arg("pages") = py::none());
+  m.def("attention_scores", &attention_scores, "accumulate KV-eviction attention scores (tcgen05)", py::arg("q"),
+        py::arg("k_cache"), py::arg("kv_len"), py::arg("n_new"), py::arg("mask"), py::arg("lse2"), py::arg("scores"),
+        py::arg("scale"), py::arg("q_offset"), py::arg("pages") = py::none());
   m.def("silu_mul", &silu_mul, "SwiGLU activation of [gate; up]");
   m.def("glu", &glu_act, "act(gate) * up of [gate; up]: act 0 = SiLU, 1 = GELU (tanh approximation)");
   m.def("linear_parts", &linear_parts, "x @ w.T as bf16 or fp32 split-K partials for a fusing consumer");
@@ -1373,7 +1457,8 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("argmax", &argmax, "row argmax");
   m.def("greedy_accept", &greedy_accept, "longest accepted path of a verified draft tree", py::arg("tokens"),
         py::arg("parents"), py::arg("pred"), py::arg("ok") = py::none());
-  m.def("kv_compact", &kv_compact, "move an accepted path's K/V to consecutive slots");
+  m.def("kv_compact", &kv_compact, "move an accepted path's K/V to consecutive slots", py::arg("cache"),
+        py::arg("kv_len"), py::arg("path"), py::arg("n_acc"), py::arg("pages") = py::none());
   m.def("sample", &sample, "inverse-CDF draw of one token per probability row");
   m.def("rejection", &rejection, "lossless speculative sampling of a draft chain (accept/reject + resample)");
   m.def("ngram", &ngram, "prompt-lookup draft proposals from the token history");

@@ -16,6 +16,8 @@
 #include <set>
 #include <utility>
 
+#include "launchers.h"  // KVPages, KVLayout
+
 namespace ecz {
 
 using bf16 = __nv_bfloat16;
@@ -28,6 +30,7 @@ enum StatusCode : unsigned {
   kStatusWaitAccum = 4u,      // epilogue gave up waiting for the accumulator
   kStatusWaitPeer = 8u,       // a fused collective gave up waiting for a peer's flag
   kStatusBadShape = 16u,      // a launch saw a shape it cannot handle (kernel returned without work)
+  kStatusBadIndex = 32u,      // an index argument lay outside its table (the kernel clamped it and reported it)
 };
 
 constexpr unsigned long long kWaitLimitNs = 2000000000ull;  // 2 s
@@ -264,6 +267,30 @@ inline cudaError_t launch_pdl(void (*kernel)(KArgs...), dim3 grid, dim3 block, s
   cfg.attrs = attr;
   cfg.numAttrs = 1;
   return cudaLaunchKernelEx(&cfg, kernel, static_cast<KArgs>(args)...);
+}
+
+// ---- KV cache addressing ----------------------------------------------------------------------------------------
+// Where the K (or V) row of (sequence b, KV head kvh, logical slot s) lives. Contiguous caches [B, Hkv, S, D]: row
+// (b Hkv + kvh) S + s. Paged caches: logical chunk s / 128 of sequence b sits in page table[b * max_chunks + s / 128]
+// of a pool whose pages start page_rows rows apart and hold the KV heads' 128-slot blocks one after another (a pool
+// [P, 2, Hkv, 128, D] of K and V pages has page_rows = 2 Hkv 128 from either base). A ring cache of a sliding-window
+// layer is a page table that maps chunk c to the row's page c mod R.
+__device__ __forceinline__ size_t kv_row(const KVPages& pg, int b, int Hkv, int kvh, int S, int s) {
+  if (pg.table == nullptr) return (static_cast<size_t>(b) * Hkv + kvh) * S + s;
+  const int page = pg.table[static_cast<size_t>(b) * pg.max_chunks + (s >> 7)];
+  return static_cast<size_t>(page) * pg.page_rows + static_cast<size_t>(kvh) * 128 + (s & 127);
+}
+
+// Every layer of a cache (kernels that touch all layers at once: KV compaction, KIVI coding). The K row of
+// (layer l, sequence b, head kvh, slot s) is l layer_rows + kv_row(l's pages, ...), its V row v_rows further.
+// Contiguous [L, 2, B, Hkv, S, D]: layer_rows = 2 B Hkv S, v_rows = B Hkv S, no table. Paged pool [P, 2, Hkv, 128,
+// D] with tables [L, B, C]: layer_rows = 0 (pages are global), v_rows = Hkv 128, table_stride = B C.
+__device__ __forceinline__ size_t kv_layer_row(const KVLayout& L, int layer, int kv, int b, int Hkv, int kvh, int S,
+                                               int s) {
+  KVPages pg = L.pages;
+  if (pg.table != nullptr) pg.table += static_cast<size_t>(layer) * L.table_stride;
+  return static_cast<size_t>(layer) * L.layer_rows + static_cast<size_t>(kv) * L.v_rows +
+         kv_row(pg, b, Hkv, kvh, S, s);
 }
 
 // ---- numerics --------------------------------------------------------------------------------------------------

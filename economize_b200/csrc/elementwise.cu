@@ -168,7 +168,8 @@ __global__ void __launch_bounds__(256) rope_store_kernel(
     const float* __restrict__ sin_t, bf16* __restrict__ q_out, bf16* __restrict__ k_cache,
     bf16* __restrict__ v_cache, const int* __restrict__ kv_len, const int* __restrict__ n_new,
     const bf16* __restrict__ q_norm, const bf16* __restrict__ k_norm, float eps, int tokens, int T, int H, int Hkv,
-    int S, int q_offset, const float* __restrict__ k_scale, const float* __restrict__ v_scale, Parts parts) {
+    int S, int q_offset, const float* __restrict__ k_scale, const float* __restrict__ v_scale, Parts parts,
+    KVPages pages, int table_rows, unsigned* status) {
   pdl_trigger();
   pdl_wait();
   // each active lane owns E consecutive elements (whole bf16 pairs) of each half of the head: D = 64 uses 16 lanes
@@ -208,7 +209,11 @@ __global__ void __launch_bounds__(256) rope_store_kernel(
     }
   }
   if (!active) return;
-  const int pos = positions[token];
+  int pos = positions[token];
+  if (pos < 0 || pos >= table_rows) {  // a position past the rotary tables: report it, never read past them
+    if (lane == 0 && status != nullptr) atomicOr(status, kStatusBadIndex);
+    pos = min(max(pos, 0), table_rows - 1);
+  }
   const float* cp = cos_t + static_cast<size_t>(pos) * (D / 2) + i0;
   const float* sp = sin_t + static_cast<size_t>(pos) * (D / 2) + i0;
   // out = x * cos + rotate_half(x) * sin, each product rounded to bf16 (HF computes it in the input dtype)
@@ -231,8 +236,11 @@ __global__ void __launch_bounds__(256) rope_store_kernel(
   const int j = q_offset + t;
   if (j >= n_new[b]) return;
   const int kvh = head - H;
-  const size_t slot = static_cast<size_t>(kv_len[b]) + j;
-  const size_t off = ((static_cast<size_t>(b) * Hkv + kvh) * S + slot) * D;
+  if (kv_len[b] + j >= S) {  // a slot past the cache: report it, never write past the cache
+    if (lane == 0 && status != nullptr) atomicOr(status, kStatusBadIndex);
+    return;
+  }
+  const size_t off = kv_row(pages, b, Hkv, kvh, S, kv_len[b] + j) * D;
   const size_t vsrc = static_cast<size_t>(token) * width + (H + Hkv) * D + kvh * D;
   if (k_scale != nullptr) {
     // fp8 cache: e4m3 codes of value / scale (quotient rounded to fp32 first, then to e4m3 with saturation)
@@ -267,8 +275,8 @@ int launch_rope_store(const void* qkv, const int* positions, const float* cos_t,
                       void* k_cache, void* v_cache, const int* kv_len, const int* n_new, const void* q_norm,
                       const void* k_norm, float eps, int B, int T, int H, int Hkv, int D, int S, int q_offset,
                       cudaStream_t stream, const float* k_scale, const float* v_scale, const float* qkv_parts,
-                      int splits) {
-  if (D != 64 && D != 128 && D != 256) return -1;
+                      int splits, const KVPages& pages, int table_rows, unsigned* status) {
+  if ((D != 64 && D != 128 && D != 256) || table_rows < 1) return -1;
   const Parts parts{qkv_parts, splits, static_cast<long>(B) * T * (H + 2 * Hkv) * D};
   const long warps = static_cast<long>(B) * T * (H + Hkv);
   const int blocks = static_cast<int>((warps * 32 + 255) / 256);
@@ -276,7 +284,7 @@ int launch_rope_store(const void* qkv, const int* positions, const float* cos_t,
   launch_pdl(kernel, dim3(blocks), dim3(256), 0, stream, static_cast<const bf16*>(qkv), positions, cos_t,
              sin_t, static_cast<bf16*>(q_out), static_cast<bf16*>(k_cache), static_cast<bf16*>(v_cache), kv_len,
              n_new, static_cast<const bf16*>(q_norm), static_cast<const bf16*>(k_norm), eps, B * T, T, H, Hkv, S,
-             q_offset, k_scale, v_scale, parts);
+             q_offset, k_scale, v_scale, parts, pages, table_rows, status);
   return 0;
 }
 
@@ -500,16 +508,16 @@ constexpr int kCompactPer = 4;
 
 __global__ void kv_compact_kernel(uint8_t* __restrict__ cache, const int* __restrict__ kv_len,
                                   const int* __restrict__ path, const int* __restrict__ n_acc, int B, int Hkv, int S,
-                                  int row_bytes, int T, int max_depth) {
+                                  int row_bytes, int T, int max_depth, KVLayout layout) {
   pdl_trigger();
   pdl_wait();
-  const int lh = blockIdx.x;  // layer*2 + kv
+  const int layer = blockIdx.x >> 1, kv = blockIdx.x & 1;
   const int b = blockIdx.y, h = blockIdx.z;
   const int n = n_acc[b];
   const int vecs = row_bytes / 16;
   const int pairs = max_depth * vecs;
-  uint8_t* base = cache + ((static_cast<size_t>(lh) * B + b) * Hkv + h) * static_cast<size_t>(S) * row_bytes;
   const int start = kv_len[b];
+  auto row = [&](int slot) { return cache + kv_layer_row(layout, layer, kv, b, Hkv, h, S, slot) * row_bytes; };
   uint4 v[kCompactPer];
   int dst[kCompactPer];
 #pragma unroll
@@ -519,8 +527,9 @@ __global__ void kv_compact_kernel(uint8_t* __restrict__ cache, const int* __rest
     dst[u] = -1;
     if (pr < pairs && i <= n && i < T) {
       const int src = path[static_cast<size_t>(b) * T + i];
+      if (start + src >= S || start + i >= S || src < 0) continue;  // never move past the cache
       if (src != i) {
-        v[u] = reinterpret_cast<const uint4*>(base + static_cast<size_t>(start + src) * row_bytes)[pr % vecs];
+        v[u] = reinterpret_cast<const uint4*>(row(start + src))[pr % vecs];
         dst[u] = i;
       }
     }
@@ -530,21 +539,21 @@ __global__ void kv_compact_kernel(uint8_t* __restrict__ cache, const int* __rest
   for (int u = 0; u < kCompactPer; ++u) {
     if (dst[u] >= 0) {
       const int pr = threadIdx.x + u * blockDim.x;
-      reinterpret_cast<uint4*>(base + static_cast<size_t>(start + dst[u]) * row_bytes)[pr % vecs] = v[u];
+      reinterpret_cast<uint4*>(row(start + dst[u]))[pr % vecs] = v[u];
     }
   }
 }
 
 // Rows of `row_bytes` bytes (D * element size: bf16 and fp8 caches alike).
-int launch_kv_compact(void* cache, const int* kv_len, const int* path, const int* n_acc, int LH, int B, int Hkv,
-                      int S, int row_bytes, int T, int max_depth, cudaStream_t stream) {
+int launch_kv_compact(void* cache, const int* kv_len, const int* path, const int* n_acc, int L, int B, int Hkv,
+                      int S, int row_bytes, int T, int max_depth, cudaStream_t stream, const KVLayout& layout) {
   if (row_bytes % 16 || max_depth < 1) return -1;
   const int pairs = max_depth * (row_bytes / 16);
   const int threads = std::min(1024, ((pairs + 31) / 32) * 32);
   if (pairs > threads * kCompactPer) return -1;
-  dim3 grid(LH, B, Hkv);
+  dim3 grid(2 * L, B, Hkv);
   launch_pdl(kv_compact_kernel, grid, dim3(threads), 0, stream, static_cast<uint8_t*>(cache), kv_len, path, n_acc,
-             B, Hkv, S, row_bytes, T, max_depth);
+             B, Hkv, S, row_bytes, T, max_depth, layout);
   return 0;
 }
 

@@ -49,6 +49,21 @@ struct AgWait {
   int world = 0;
 };
 
+// Paged KV caches: where (sequence, KV head, logical slot) rows live; the device-side mapping is kv_row /
+// kv_layer_row in common.cuh, which documents the layouts.
+struct KVPages {
+  const int* table = nullptr;
+  int max_chunks = 0;
+  int page_rows = 0;
+};
+
+struct KVLayout {
+  KVPages pages;
+  long table_stride = 0;
+  long layer_rows = 0;
+  long v_rows = 0;
+};
+
 // Score options of an attention launch: tanh soft-cap of the scaled scores (0: off), one sink logit per query head
 // (fp32 [H], natural-log units; nullptr: off), sliding window in positions (0: off).
 struct AttnOpts {
@@ -74,7 +89,8 @@ int launch_rope_store(const void* qkv, const int* positions, const float* cos_t,
                       void* k_cache, void* v_cache, const int* kv_len, const int* n_new, const void* q_norm,
                       const void* k_norm, float eps, int B, int T, int H, int Hkv, int D, int S, int q_offset,
                       cudaStream_t stream, const float* k_scale = nullptr, const float* v_scale = nullptr,
-                      const float* qkv_parts = nullptr, int splits = 0);
+                      const float* qkv_parts = nullptr, int splits = 0, const KVPages& pages = KVPages(),
+                      int table_rows = 1 << 30, unsigned* status = nullptr);
 // act(gate) * up of a fused [gate; up] projection: act 0 = SiLU, 1 = GELU (tanh approximation)
 int launch_glu(const void* gu, void* out, int rows, int F, cudaStream_t stream, const float* gu_parts, int splits,
                int act);
@@ -86,8 +102,8 @@ int launch_argmax(const void* x, bool is_bf16, int64_t* out, float* part_v, int*
 // ok [B, T] (optional): node t is acceptable given its parent; without it, tokens[t] == pred[parent].
 int launch_greedy_accept(const int64_t* tokens, const int64_t* parents, const int64_t* pred, const uint8_t* ok,
                          int* n_acc, int* path, int64_t* out, int B, int T, cudaStream_t stream);
-int launch_kv_compact(void* cache, const int* kv_len, const int* path, const int* n_acc, int LH, int B, int Hkv,
-                      int S, int row_bytes, int T, int max_depth, cudaStream_t stream);
+int launch_kv_compact(void* cache, const int* kv_len, const int* path, const int* n_acc, int L, int B, int Hkv,
+                      int S, int row_bytes, int T, int max_depth, cudaStream_t stream, const KVLayout& layout);
 
 // gemm_tc.cu
 int gemm_block_n(int M);
@@ -122,16 +138,18 @@ int launch_attention(const void* q, const CUtensorMap* tm_k, const CUtensorMap* 
                      const float* v_scale = nullptr, const uint32_t* keep = nullptr, float* lse_out = nullptr,
                      const uint8_t* kivi = nullptr, const int* kivi_chunks = nullptr, int kivi_bits = 0,
                      int tail_w = 0, const void* k_cache = nullptr, const void* v_cache = nullptr,
-                     const AttnOpts& opts = AttnOpts());
+                     const AttnOpts& opts = AttnOpts(), const KVPages& pages = KVPages());
 // KIVI: bytes of one quantized 128-key chunk; quantise committed chunks of a bf16 cache [L, 2, B, Hkv, S, D] into
 // kivi [L, B, Hkv, S / 128, chunk bytes] and advance chunks [B] (at most max_new chunks per row and call)
 int kivi_chunk_size(int bits);
 int launch_kivi_quantize(const void* cache, void* kivi, const int* kv_len, int* chunks, int L, int B, int Hkv, int S,
-                         int D, int bits, int residual, int max_new, cudaStream_t stream);
+                         int D, int bits, int residual, int max_new, cudaStream_t stream,
+                         const KVLayout& layout);
 // KV-eviction scores: scores[b, kvh, s] += attention probability mass of slot s (see attention.cu)
 int launch_attention_scores(const void* q, const CUtensorMap* tm_k, const float* lse2, float* scores,
                             const int* kv_len, const int* n_new, const int64_t* mask, int B, int T, int H, int Hkv,
-                            int D, int S, float scale, int q_offset, unsigned* status, cudaStream_t stream);
+                            int D, int S, float scale, int q_offset, unsigned* status, cudaStream_t stream,
+                            const KVPages& pages = KVPages());
 
 // sampling.cu
 int launch_topk_logp(const float* logits, const int64_t* d2t, float* vals, int64_t* ids, int rows, int V, int k,

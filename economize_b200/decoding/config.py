@@ -41,8 +41,11 @@ class DecodeConfig:
             ``cuda_graphs`` is on.
         draft_policy_options: Options of the draft policy (``{"depth": 6, "topk": 10, "total_tokens": 60}``).
         prefill_chunk: Prefill prompts in chunks of this many tokens.
-        window_cache: Ring caches for sliding-window layers. This engine keeps one contiguous slot cache for every
-            layer, so ``True`` is refused with :class:`~economize_b200.errors.ConfigError` rather than ignored.
+        window_cache: Ring caches for sliding-window layers: the cache becomes a page pool and every windowed
+            layer keeps a ring of pages covering its window (its memory follows the window, not the context);
+            prompts longer than the ring's reserve are prefilled in chunks.
+        kv_pages: Keep the KV cache in a pool of 128-slot pages addressed through per-layer page tables (the
+            paged layout of serving engines; implied by ``window_cache``).
     """
 
     cycle_length: int = 4
@@ -59,15 +62,13 @@ class DecodeConfig:
     draft_policy_options: Mapping[str, object] = field(default_factory=dict, hash=False)
     prefill_chunk: int | None = None
     window_cache: bool = False
+    kv_pages: bool = False
 
     def __post_init__(self) -> None:
         check_positive("cycle_length", self.cycle_length)
         check_positive("sync_interval", self.sync_interval)
         if self.prefill_chunk is not None:
             check_positive("prefill_chunk", self.prefill_chunk)
-        if self.window_cache:
-            raise ConfigError("window_cache=True asks for ring caches of sliding-window layers, which this engine "
-                              "does not build (every layer keeps a contiguous slot cache); leave it False")
         if self.min_confidence is not None:
             check_unit_interval("min_confidence", self.min_confidence, closed_high=True)
         for name in ("verifier_options", "draft_policy_options"):

@@ -27,7 +27,7 @@ import torch
 from .. import ops
 from ..errors import ConfigError
 from ..models.llama import CausalLM
-from ..runtime.cache import KVCache, StepBatch
+from ..runtime.cache import KVCache, PagedKVCache, StepBatch
 from ..runtime.phase import phase
 from .config import DecodeConfig
 from .drafter import DraftModel
@@ -103,10 +103,10 @@ class _State:
     """Persistent device buffers of one (batch, capacity) configuration (graph inputs and outputs)."""
 
     def __init__(self, model: CausalLM, drafter: DraftModel | None, batch: int, capacity: int, out_cap: int,
-                 draft_vocab: int) -> None:
+                 draft_vocab: int, layout: dict | None = None) -> None:
         dev = model.device
         self.batch, self.capacity, self.out_cap = batch, capacity, out_cap
-        self.cache: KVCache = model.new_cache(batch, capacity)
+        self.cache: KVCache | PagedKVCache = model.new_cache(batch, capacity, **(layout or {}))
         i32 = dict(dtype=torch.int32, device=dev)
         self.kv_len = torch.zeros(batch, **i32)
         self.last = torch.zeros(batch, dtype=torch.int64, device=dev)
@@ -300,6 +300,24 @@ class SpecEngine:
         return log
 
     # ---- state -------------------------------------------------------------------------------------------------
+    @property
+    def paged(self) -> bool:
+        return bool(self.config.window_cache or self.config.kv_pages)
+
+    def ring_reserve(self) -> int:
+        """New slots one pass of this engine may write into a ring cache: a prefill chunk or a verification tree."""
+        chunk = self.config.prefill_chunk or 512
+        return int(math.ceil(max(chunk, self.nodes + self.depth + 2) / 128) * 128)
+
+    def _layout(self) -> dict | None:
+        if not self.paged:
+            return None
+        m = self.model
+        if m.kv_evictor is not None or m.prefill_sparsity is not None:
+            raise ConfigError("paged and ring caches do not serve keep-bitmap KV techniques (eviction, sparse "
+                              "views); use the contiguous cache (window_cache=False, kv_pages=False)")
+        return dict(paged=True, rings=self.config.window_cache, reserve=self.ring_reserve())
+
     def _state(self, batch: int, capacity: int, out_cap: int) -> _State:
         key = (batch, capacity, out_cap)
         st = self._states.get(key)
@@ -307,7 +325,7 @@ class SpecEngine:
             # one live configuration at a time keeps memory bounded; graphs of other shapes are dropped
             self._states = {k: v for k, v in self._states.items() if k[0] == batch}
             self._graphs = {k: v for k, v in self._graphs.items() if k in self._states}
-            st = _State(self.model, self.drafter, batch, capacity, out_cap, self.draft_vocab)
+            st = _State(self.model, self.drafter, batch, capacity, out_cap, self.draft_vocab, self._layout())
             self._states[key] = st
         else:
             st.cache.reset()
@@ -326,6 +344,8 @@ class SpecEngine:
         batch, width = prompts.shape
         capture = drafter.capture_layers if drafter is not None else ()
         chunk = self.config.prefill_chunk
+        if self.config.window_cache and any(getattr(st.cache, "rings", ())):
+            chunk = min(chunk or st.cache.reserve, st.cache.reserve)  # a pass may not lap a ring
         model.begin_sequence(st.cache)
         with phase("prefill"):
             if chunk is not None and width > chunk:
@@ -477,7 +497,7 @@ class SpecEngine:
             after(tokens, self.last_pred)
         if self.acceptance is not None:  # Sequoia rate measurement: one host synchronization per cycle
             record_cycle(self.acceptance, self.static_tree, self._plan(dev), tokens, path, n_acc, out)
-        ops.kv_compact(st.cache.data, st.kv_len, path, n_acc)
+        ops.kv_compact(st.cache.data, st.kv_len, path, n_acc, st.cache.tables)
         # ---- commit ----
         active = st.n_out < st.max_new
         width = depth + 1

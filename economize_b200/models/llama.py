@@ -25,7 +25,7 @@ from torch import nn
 
 from .. import ops
 from ..errors import ConfigError
-from ..runtime.cache import KVCache, StepBatch
+from ..runtime.cache import KVCache, PagedKVCache, StepBatch
 from .config import ModelConfig, rope_inv_freq
 
 __all__ = ["CausalLM", "DecoderLayer", "init_weights"]
@@ -150,11 +150,17 @@ class CausalLM(nn.Module):
             return self.rope_tables(cos.shape[0], local=True)
         return cos, sin
 
-    def new_cache(self, batch: int, capacity: int) -> KVCache:
+    def new_cache(self, batch: int, capacity: int, paged: bool = False, rings: bool = False,
+                  reserve: int = 512) -> KVCache | PagedKVCache:
         """A zeroed cache in the model's KV format (``kv_dtype``: the compute dtype, or fp8 e4m3 with the per-head
-        ``kv_scales`` a KV technique set)."""
+        ``kv_scales`` a KV technique set). ``paged``: a page pool with one page table per layer; ``rings``: the
+        sliding-window layers get ring tables of their window (plus ``reserve`` slots a pass may write)."""
         c = self.config
         dtype = self.kv_dtype or self.dtype
+        if paged or rings:
+            windows = [c.window_of(i) for i in range(c.num_layers)] if rings else None
+            return PagedKVCache(c.num_layers, batch, self.local["num_kv_heads"], capacity, c.head_dim, dtype,
+                                self.device, self.kv_scales, windows=windows, reserve=reserve)
         return KVCache(c.num_layers, batch, self.local["num_kv_heads"], capacity, c.head_dim, dtype, self.device,
                        self.kv_scales)
 
@@ -196,7 +202,7 @@ class CausalLM(nn.Module):
             return self._forward_sp(tokens, batch, cache, capture)
         if c.post_norm or c.sandwich_norm:
             return self._forward_post_norm(tokens, batch, cache, capture, layers, hidden)
-        cos, sin = self.rope_tables()
+        cos, sin = self.rope_tables(cache.capacity)  # every slot's position has a row
         h = self.embed_tokens(tokens) if hidden is None else hidden
         resid: torch.Tensor | None = None
         aux: dict[int, torch.Tensor] = {}
@@ -254,7 +260,7 @@ class CausalLM(nn.Module):
         then the final norm."""
         c = self.config
         eps = c.rms_norm_eps
-        cos, sin = self.rope_tables()
+        cos, sin = self.rope_tables(cache.capacity)  # every slot's position has a row
         h = self.embed_tokens(tokens) if hidden is None else hidden
         aux: dict[int, torch.Tensor] = {}
         sandwich = c.sandwich_norm
@@ -299,7 +305,7 @@ class CausalLM(nn.Module):
         eps = c.rms_norm_eps
         B, T = tokens.shape
         M = B * T
-        cos, sin = self.rope_tables()
+        cos, sin = self.rope_tables(cache.capacity)  # every slot's position has a row
         emb = self.embed_tokens(tokens)
         lo, n = sp.shard(M)
         resid = emb.reshape(M, -1)[lo:lo + n].contiguous()
@@ -378,6 +384,7 @@ class CausalLM(nn.Module):
         outputs ``[B, T, H_q * D]`` (this rank's heads under tensor parallelism)."""
         c = self.config
         k_cache, v_cache = cache.layer(index)
+        pages = cache.pages(index)  # a paged cache's table (None: contiguous)
         k_scale, v_scale = cache.layer_scales(index)
         q_norm, k_norm = layer.q_norm, layer.k_norm
         if c.qk_norm_full and q_norm is not None:  # RMSNorm over all heads' features of q and of k (OLMo-2)
@@ -393,7 +400,7 @@ class CausalLM(nn.Module):
         q = ops.rope_store(qkv, batch.positions, cos, sin, self.local["num_heads"], self.local["num_kv_heads"],
                            c.head_dim, k_cache,
                            v_cache, batch.kv_len, batch.n_new, q_norm, k_norm, c.rms_norm_eps,
-                           q_offset=batch.q_offset, k_scale=k_scale, v_scale=v_scale)
+                           q_offset=batch.q_offset, k_scale=k_scale, v_scale=v_scale, pages=pages)
         keep = self.kv_evictor.keep_for(index, k_cache, q, batch) if self.kv_evictor is not None else None
         sparse = self.prefill_sparsity
         if sparse is not None and sparse.active:  # sparse prefill (MInference): keys the chunk's pattern hides
@@ -405,7 +412,8 @@ class CausalLM(nn.Module):
         tail = self.exact_tail if (not batch.prompt and q.shape[1] <= 64 and not sparse_pass) else 0
         o = ops.attention(q, k_cache, v_cache, batch.kv_len, batch.n_new, batch.mask, scale=c.attention_multiplier,
                           q_offset=batch.q_offset, k_scale=k_scale, v_scale=v_scale, keep=keep, tail=tail,
-                          softcap=c.attn_softcap, sinks=layer.sinks, window=c.window_of(index), **kivi)
+                          softcap=c.attn_softcap, sinks=layer.sinks, window=c.window_of(index), pages=pages,
+                          **kivi)
         if self.kv_evictor is not None and batch.is_prefill:
             self.kv_evictor.observe_prefill(index, q, k_cache, v_cache, batch)
         return o.reshape(*o.shape[:2], -1)
@@ -435,7 +443,7 @@ class CausalLM(nn.Module):
                           getattr(self, "ep", None), renormalize=self.config.norm_topk_prob)
             if layer.w_shared_gate_up is not None:  # Qwen2-MoE's gated shared expert
                 shared = ops.linear(ops.silu_mul(ops.linear(x, layer.w_shared_gate_up)), layer.w_shared_down)
-                gate = torch.sigmoid(ops.linear(x, layer.shared_gate))
+                gate = torch.sigmoid(ops.linear(x, self._gate_rows(layer))[..., :1])
                 out = out + gate * shared
             return out
         if self.observer is not None:
@@ -450,12 +458,25 @@ class CausalLM(nn.Module):
             self.observer(index, "w_down", a)
         return self._row_linear(a, layer.w_down)
 
+    @staticmethod
+    def _gate_rows(layer: DecoderLayer) -> torch.Tensor:
+        """The shared expert's gate vector as the first of four rows (the GEMM kernels take N in multiples of 4;
+        the zero rows cost nothing next to the expert GEMMs)."""
+        w = layer.shared_gate
+        if not w.is_cuda:
+            return w
+        key = (w.data_ptr(), w._version)
+        if getattr(layer, "_gate4_key", None) != key:
+            layer._gate4 = torch.cat([w.detach(), w.new_zeros(3, w.shape[1])], 0)
+            layer._gate4_key = key
+        return layer._gate4
+
     def begin_sequence(self, cache: KVCache) -> None:
         """A new generation starts in ``cache`` (slot 0 on)."""
         if self.kv_quantizer is not None:
             self.kv_quantizer.reset(cache)
 
-    def after_commit(self, cache: KVCache, kv_len: torch.Tensor, prefill: bool = False) -> None:
+    def after_commit(self, cache: KVCache | PagedKVCache, kv_len: torch.Tensor, prefill: bool = False) -> None:
         """Tokens up to ``kv_len`` are committed (KV coders compress what became old)."""
         if self.kv_quantizer is not None:
             self.kv_quantizer.after_commit(cache, kv_len, max(1, cache.capacity // 128) if prefill else 1)

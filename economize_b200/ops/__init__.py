@@ -112,14 +112,16 @@ def rope_store(qkv: torch.Tensor, positions: torch.Tensor, cos: torch.Tensor, si
                num_kv_heads: int, head_dim: int, k_cache: torch.Tensor, v_cache: torch.Tensor,
                kv_len: torch.Tensor, n_new: torch.Tensor, q_norm: torch.Tensor | None = None,
                k_norm: torch.Tensor | None = None, eps: float = 1e-6, q_offset: int = 0,
-               k_scale: torch.Tensor | None = None, v_scale: torch.Tensor | None = None) -> torch.Tensor:
+               k_scale: torch.Tensor | None = None, v_scale: torch.Tensor | None = None,
+               pages: torch.Tensor | None = None) -> torch.Tensor:
     """Fused (per-head RMSNorm +) rotary embedding of queries and keys and the KV-cache write (see
-    :func:`.reference.rope_store`); fp8 caches are written as e4m3 codes of ``value / scale``."""
+    :func:`.reference.rope_store`); fp8 caches are written as e4m3 codes of ``value / scale``; ``pages``: paged
+    caches (as for :func:`attention`)."""
     if qkv.is_cuda:
         return require().rope_store(_raw(qkv), positions, cos, sin, num_heads, num_kv_heads, head_dim, k_cache, v_cache,
-                                    kv_len, n_new, q_norm, k_norm, float(eps), int(q_offset), k_scale, v_scale)
+                                    kv_len, n_new, q_norm, k_norm, float(eps), int(q_offset), k_scale, v_scale, pages)
     return reference.rope_store(qkv, positions, cos, sin, num_heads, num_kv_heads, head_dim, k_cache, v_cache,
-                                kv_len, n_new, q_norm, k_norm, eps, q_offset, k_scale, v_scale)
+                                kv_len, n_new, q_norm, k_norm, eps, q_offset, k_scale, v_scale, pages)
 
 
 def attention(q: torch.Tensor, k_cache: torch.Tensor, v_cache: torch.Tensor, kv_len: torch.Tensor,
@@ -128,12 +130,15 @@ def attention(q: torch.Tensor, k_cache: torch.Tensor, v_cache: torch.Tensor, kv_
               v_scale: torch.Tensor | None = None, keep: torch.Tensor | None = None,
               lse_out: torch.Tensor | None = None, kivi: torch.Tensor | None = None,
               kivi_chunks: torch.Tensor | None = None, kivi_bits: int = 0, tail: int = 0,
-              softcap: float | None = None, sinks: torch.Tensor | None = None, window: int = 0) -> torch.Tensor:
+              softcap: float | None = None, sinks: torch.Tensor | None = None, window: int = 0,
+              pages: torch.Tensor | None = None) -> torch.Tensor:
     """Causal / tree-masked attention over the slot cache (see :func:`.reference.attention`); fp8 caches take
     per-KV-head scales, ``keep`` (int32 bit words ``[B, H_kv, S / 32]``) hides evicted committed slots and
     ``lse_out [B, T, H]`` receives every row's log2-domain log-sum-exp. ``softcap`` (tanh soft-capping of the
     scores), ``sinks`` (fp32 ``[H]`` sink logits) and ``window`` (sliding window in positions; the kernel then reads
     only the window's chunks) serve Gemma-2, gpt-oss and the sliding-window layers of Mistral, Gemma-2/3 and OLMo-3.
+    ``pages [B, C]`` (int32): the caches are views ``[P, H_kv, 128, D]`` of a page pool and logical chunk ``c`` of row
+    ``b`` is page ``pages[b, c]`` (:class:`~economize_b200.runtime.cache.PagedKVCache`).
 
     ``tail > 0`` (passes of at most 64 queries) reduces the keys at the last ``tail`` positions before each query,
     and its own new keys, one at a time in position order: a verification pass then computes every query bit for
@@ -145,10 +150,10 @@ def attention(q: torch.Tensor, k_cache: torch.Tensor, v_cache: torch.Tensor, kv_
     if q.is_cuda:
         return require().attention(q, k_cache, v_cache, kv_len, n_new, mask, scale, int(q_offset), None, k_scale,
                                    v_scale, keep, lse_out, kivi, kivi_chunks, int(kivi_bits), int(tail),
-                                   float(softcap or 0.0), sinks, window)
+                                   float(softcap or 0.0), sinks, window, pages)
     return reference.attention(q, k_cache, v_cache, kv_len, n_new, mask, scale, softcap=softcap, q_offset=q_offset,
                                k_scale=k_scale, v_scale=v_scale, keep=keep, lse_out=lse_out, kivi=kivi,
-                               kivi_chunks=kivi_chunks, kivi_bits=kivi_bits, sinks=sinks, window=window)
+                               kivi_chunks=kivi_chunks, kivi_bits=kivi_bits, sinks=sinks, window=window, pages=pages)
 
 
 _ATTENTION_USAGE: dict[tuple[str, str, int, str], int] = {}
@@ -183,23 +188,24 @@ def attention_usage(reset: bool = False) -> dict[tuple[str, str, int, str], int]
 
 
 def kivi_quantize(cache: torch.Tensor, kivi: torch.Tensor, kv_len: torch.Tensor, chunks: torch.Tensor, bits: int,
-                  residual: int, max_new: int) -> None:
-    """Code newly committed 128-key chunks of every layer into KIVI storage and advance ``chunks`` (in place)."""
+                  residual: int, max_new: int, pages: torch.Tensor | None = None) -> None:
+    """Code newly committed 128-key chunks of every layer into KIVI storage and advance ``chunks`` (in place);
+    ``pages [L, B, C]``: ``cache`` is a page pool ``[P, 2, H_kv, 128, D]``."""
     if cache.is_cuda:
-        require().kivi_quantize(cache, kivi, kv_len, chunks, int(bits), int(residual), int(max_new))
+        require().kivi_quantize(cache, kivi, kv_len, chunks, int(bits), int(residual), int(max_new), pages)
         return
-    reference.kivi_quantize(cache, kivi, kv_len, chunks, bits, residual, max_new)
+    reference.kivi_quantize(cache, kivi, kv_len, chunks, bits, residual, max_new, pages)
 
 
 def attention_scores(q: torch.Tensor, k_cache: torch.Tensor, kv_len: torch.Tensor, n_new: torch.Tensor,
                      mask: torch.Tensor | None, lse2: torch.Tensor, scores: torch.Tensor,
-                     scale: float | None = None, q_offset: int = 0) -> None:
+                     scale: float | None = None, q_offset: int = 0, pages: torch.Tensor | None = None) -> None:
     """Accumulate KV-eviction scores (H2O / SnapKV) into ``scores [B, H_kv, S]`` on the tensor cores."""
     scale = float(scale if scale is not None else q.shape[-1] ** -0.5)
     if q.is_cuda:
-        require().attention_scores(q, k_cache, kv_len, n_new, mask, lse2, scores, scale, int(q_offset))
+        require().attention_scores(q, k_cache, kv_len, n_new, mask, lse2, scores, scale, int(q_offset), pages)
         return
-    reference.attention_scores(q, k_cache, kv_len, n_new, mask, lse2, scores, scale, q_offset)
+    reference.attention_scores(q, k_cache, kv_len, n_new, mask, lse2, scores, scale, q_offset, pages)
 
 
 def silu_mul(gate_up: torch.Tensor | Partials) -> torch.Tensor:
@@ -254,12 +260,14 @@ def greedy_accept(tokens: torch.Tensor, parents: torch.Tensor, pred: torch.Tenso
     return reference.greedy_accept(tokens, parents, pred, ok)
 
 
-def kv_compact(cache: torch.Tensor, kv_len: torch.Tensor, path: torch.Tensor, n_acc: torch.Tensor) -> None:
-    """Move an accepted path's cache entries to consecutive slots in every layer (in place)."""
+def kv_compact(cache: torch.Tensor, kv_len: torch.Tensor, path: torch.Tensor, n_acc: torch.Tensor,
+               pages: torch.Tensor | None = None) -> None:
+    """Move an accepted path's cache entries to consecutive slots in every layer (in place); ``pages [L, B, C]``:
+    ``cache`` is a page pool ``[P, 2, H_kv, 128, D]``."""
     if cache.is_cuda:
-        require().kv_compact(cache, kv_len, path, n_acc)
+        require().kv_compact(cache, kv_len, path, n_acc, pages)
         return
-    reference.kv_compact(cache, kv_len, path, n_acc)
+    reference.kv_compact(cache, kv_len, path, n_acc, pages)
 
 
 def sample(probs: torch.Tensor, u: torch.Tensor) -> torch.Tensor:

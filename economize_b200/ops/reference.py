@@ -43,11 +43,24 @@ def _rotate(x: torch.Tensor, cos: torch.Tensor, sin: torch.Tensor) -> torch.Tens
     return x * c + rot * s
 
 
+def paged_logical(pool: torch.Tensor, pages: torch.Tensor) -> torch.Tensor:
+    """A logical ``[B, H_kv, C * 128, D]`` copy of one layer's K (or V) pool view ``[P, H_kv, 128, D]`` read through its
+    page table ``[B, C]`` (chunks that share a ring page repeat it)."""
+    blocks = pool[pages.long()]  # [B, C, H_kv, 128, D]
+    b, c, h, w, d = blocks.shape
+    return blocks.permute(0, 2, 1, 3, 4).reshape(b, h, c * w, d)
+
+
+def _paged_slot(pages: torch.Tensor, b: int, slot: int) -> tuple[int, int]:
+    return int(pages[b, slot // 128]), slot % 128
+
+
 def rope_store(qkv: torch.Tensor, positions: torch.Tensor, cos: torch.Tensor, sin: torch.Tensor, num_heads: int,
                num_kv_heads: int, head_dim: int, k_cache: torch.Tensor, v_cache: torch.Tensor,
                kv_len: torch.Tensor, n_new: torch.Tensor, q_norm: torch.Tensor | None = None,
                k_norm: torch.Tensor | None = None, eps: float = 1e-6, q_offset: int = 0,
-               k_scale: torch.Tensor | None = None, v_scale: torch.Tensor | None = None) -> torch.Tensor:
+               k_scale: torch.Tensor | None = None, v_scale: torch.Tensor | None = None,
+               pages: torch.Tensor | None = None) -> torch.Tensor:
     """Rotate queries and keys of ``qkv [B, T, (H + 2 H_kv) D]`` (optionally after a per-head RMSNorm), write the keys
     and values of token ``t`` to cache slot ``kv_len[b] + q_offset + t`` of ``k_cache/v_cache [B, H_kv, S, D]`` when
     ``q_offset + t < n_new[b]``, and return the rotated queries ``[B, T, H, D]``. fp8 caches store
@@ -69,7 +82,12 @@ def rope_store(qkv: torch.Tensor, positions: torch.Tensor, cos: torch.Tensor, si
         v = (v.to(torch.bfloat16).float() / v_scale.float()[:, None]).clamp(-448, 448)
     for b in range(batch):
         n, start = min(int(n_new[b]) - q_offset, length), int(kv_len[b]) + q_offset
-        if n > 0:
+        if n > 0 and pages is not None:  # paged pool views [P, H_kv, 128, D]
+            for i in range(n):
+                page, row = _paged_slot(pages, b, start + i)
+                k_cache[page, :, row] = k[b, i].to(k_cache.dtype)
+                v_cache[page, :, row] = v[b, i].to(v_cache.dtype)
+        elif n > 0:
             k_cache[b, :, start:start + n] = k[b, :n].transpose(0, 1).to(k_cache.dtype)
             v_cache[b, :, start:start + n] = v[b, :n].transpose(0, 1).to(v_cache.dtype)
     return q
@@ -117,7 +135,7 @@ def attention(q: torch.Tensor, k_cache: torch.Tensor, v_cache: torch.Tensor, kv_
               v_scale: torch.Tensor | None = None, keep: torch.Tensor | None = None,
               lse_out: torch.Tensor | None = None, kivi: torch.Tensor | None = None,
               kivi_chunks: torch.Tensor | None = None, kivi_bits: int = 0, sinks: torch.Tensor | None = None,
-              window: int = 0) -> torch.Tensor:
+              window: int = 0, pages: torch.Tensor | None = None) -> torch.Tensor:
     """Attention of queries ``[B, T, H, D]`` over the slot cache ``[B, H_kv, S, D]`` (bf16, fp32, or e4m3 codes with
     per-KV-head scales ``k_scale``/``v_scale``).
 
@@ -127,6 +145,8 @@ def attention(q: torch.Tensor, k_cache: torch.Tensor, v_cache: torch.Tensor, kv_
     to ``softcap * tanh(s / softcap)``; ``sinks [H]`` adds one logit per query head to the softmax denominator (it
     carries no value); ``window`` hides keys more than ``window - 1`` positions behind the query.
     """
+    if pages is not None:  # paged pool views: read the logical caches through the page table
+        k_cache, v_cache = paged_logical(k_cache, pages), paged_logical(v_cache, pages)
     batch, length, heads, dim = q.shape
     kv_heads = k_cache.shape[1]
     width = max(int((kv_len + n_new).max()), 1)
@@ -238,11 +258,23 @@ def greedy_accept(tokens: torch.Tensor, parents: torch.Tensor, pred: torch.Tenso
     return n_acc.to(torch.int32), path.to(torch.int32), out
 
 
-def kv_compact(cache: torch.Tensor, kv_len: torch.Tensor, path: torch.Tensor, n_acc: torch.Tensor) -> None:
+def kv_compact(cache: torch.Tensor, kv_len: torch.Tensor, path: torch.Tensor, n_acc: torch.Tensor,
+               pages: torch.Tensor | None = None) -> None:
     """Move the cache entries of an accepted tree path to consecutive slots: slot ``kv_len + path[b, i]`` to
-    ``kv_len + i`` for ``i <= n_acc[b]``, in every layer of ``cache [L, 2, B, H_kv, S, D]``."""
+    ``kv_len + i`` for ``i <= n_acc[b]``, in every layer of ``cache [L, 2, B, H_kv, S, D]`` (or of a page pool
+    ``[P, 2, H_kv, 128, D]`` with page tables ``pages [L, B, C]``)."""
     if cache.dtype == torch.float8_e4m3fn:
         cache = cache.view(torch.uint8)
+    if pages is not None:
+        for layer in range(pages.shape[0]):
+            for b in range(pages.shape[1]):
+                n, base = int(n_acc[b]), int(kv_len[b])
+                src = [_paged_slot(pages[layer], b, base + int(p)) for p in path[b, : n + 1]]
+                moved = [cache[page, :, :, row].clone() for page, row in src]
+                for i, value in enumerate(moved):
+                    page, row = _paged_slot(pages[layer], b, base + i)
+                    cache[page, :, :, row] = value
+        return
     for b in range(cache.shape[2]):
         n, base = int(n_acc[b]), int(kv_len[b])
         src = base + path[b, : n + 1].long()
@@ -320,9 +352,11 @@ def ngram(history: torch.Tensor, length: torch.Tensor, k: int, min_n: int, max_n
 
 def attention_scores(q: torch.Tensor, k_cache: torch.Tensor, kv_len: torch.Tensor, n_new: torch.Tensor,
                      mask: torch.Tensor | None, lse2: torch.Tensor, scores: torch.Tensor, scale: float,
-                     q_offset: int = 0) -> None:
+                     q_offset: int = 0, pages: torch.Tensor | None = None) -> None:
     """``scores [B, H_kv, S] +=`` the attention probability mass every visible slot receives from the queries
     ``q [B, T, H, D]`` (probabilities ``exp2(s * scale * log2 e - lse2)``), summed over each KV head's group."""
+    if pages is not None:
+        k_cache = paged_logical(k_cache, pages)
     batch, length, heads, dim = q.shape
     kv_heads, width = k_cache.shape[1], scores.shape[-1]
     group = heads // kv_heads
@@ -334,10 +368,15 @@ def attention_scores(q: torch.Tensor, k_cache: torch.Tensor, kv_len: torch.Tenso
 
 
 def kivi_quantize(cache: torch.Tensor, kivi: torch.Tensor, kv_len: torch.Tensor, chunks: torch.Tensor, bits: int,
-                  residual: int, max_new: int) -> None:
+                  residual: int, max_new: int, pages: torch.Tensor | None = None) -> None:
     """Code the committed chunks ``chunks[b] .. `` of ``cache [L, 2, B, H_kv, S, D]`` that lie at least
-    ``residual`` slots behind ``kv_len[b]`` (at most ``max_new`` per row) into ``kivi [L, B, H_kv, S/128, bytes]``."""
+    ``residual`` slots behind ``kv_len[b]`` (at most ``max_new`` per row) into ``kivi [L, B, H_kv, S/128, bytes]``
+    (a page pool ``[P, 2, H_kv, 128, D]`` with tables ``pages [L, B, C]`` is read through them)."""
     from .kivi import pack_chunks
+
+    if pages is not None:
+        cache = torch.stack([torch.stack([paged_logical(cache[:, kv], pages[layer]) for kv in (0, 1)])
+                             for layer in range(pages.shape[0])])
 
     for b in range(cache.shape[2]):
         ready = max(0, (int(kv_len[b]) - residual) // 128)

@@ -1,4 +1,4 @@
-"""The slot-addressed KV cache of the engine.
+"""The slot-addressed KV caches of the engine: contiguous (:class:`KVCache`) and paged (:class:`PagedKVCache`).
 
 One tensor ``[L, 2, B, H_kv, S, D]`` holds every layer's keys and values: row ``b`` keeps position ``p`` of its
 committed sequence in slot ``p`` (economize's ``KVCache`` layout, ``src/economize/runtime/cache.py:158``, without
@@ -16,7 +16,10 @@ from dataclasses import dataclass
 
 import torch
 
-__all__ = ["KVCache", "StepBatch"]
+__all__ = ["KVCache", "PAGE", "PagedKVCache", "StepBatch", "ring_pages"]
+
+#: slots per page of a paged cache (one key tile of the attention kernel)
+PAGE = 128
 
 
 class KVCache:
@@ -52,6 +55,99 @@ class KVCache:
 
     def reset(self) -> None:
         self.data.zero_()
+
+    def pages(self, index: int) -> None:
+        """A contiguous cache has no page table."""
+        return None
+
+    tables = None
+    paged = False
+
+
+def ring_pages(window: int, reserve: int) -> int:
+    """Pages of a ring that serves a sliding window of ``window`` positions while a pass writes up to ``reserve``
+    new slots: the window and the pass's tokens, plus one page for the window's misaligned first page."""
+    return (window + reserve + PAGE - 1) // PAGE + 1
+
+
+class PagedKVCache:
+    """Keys and values in a pool of 128-slot pages shared by every layer and row: ``data [P, 2, H_kv, 128, D]``
+    (page ``p`` holds K and V of one (layer, row) block of 128 consecutive slots) and one page table per layer,
+    ``tables [L, B, C]`` int32 (logical chunk ``c`` of row ``b`` in layer ``l`` lives in page ``tables[l, b, c]``).
+
+    A layer of a full-attention model gets one page per chunk of its capacity. A sliding-window layer whose window
+    is given in ``windows`` gets a ring instead: ``R = ring_pages(window, reserve)`` pages per row and chunk ``c``
+    in page ``c mod R`` (the ring cache of economize's ``RingSpec``, ``src/economize/runtime/cache.py:72-135``), so
+    its memory follows the window, not the context. ``reserve`` bounds the new slots one pass writes (a tree pass,
+    or a prefill chunk: longer prompts must be prefilled in chunks of at most ``reserve`` tokens), which keeps every
+    key a pass can see out of the pages it overwrites.
+
+    The attention, rotary-store, compaction, KIVI and eviction-score kernels read the tables (``kv_row`` in
+    ``csrc/common.cuh``); :meth:`layer` returns the pool views those ops take with :meth:`pages`.
+    """
+
+    paged = True
+
+    def __init__(self, num_layers: int, batch: int, num_kv_heads: int, capacity: int, head_dim: int,
+                 dtype: torch.dtype, device: torch.device | str,
+                 scales: tuple[torch.Tensor, torch.Tensor] | None = None, windows: list[int] | None = None,
+                 reserve: int = 512) -> None:
+        self.num_layers, self.batch, self.num_kv_heads, self.head_dim = num_layers, batch, num_kv_heads, head_dim
+        chunks = (capacity + PAGE - 1) // PAGE
+        self.capacity = chunks * PAGE
+        self.reserve = reserve
+        windows = list(windows or [0] * num_layers)
+        self.rings = [min(chunks, ring_pages(w, reserve)) if w else 0 for w in windows]
+        tables = torch.empty(num_layers, batch, chunks, dtype=torch.int32)
+        first = 0
+        col = torch.arange(chunks)
+        for layer in range(num_layers):
+            per_row = self.rings[layer] or chunks
+            for b in range(batch):
+                tables[layer, b] = first + col % per_row
+                first += per_row
+        self.tables = tables.to(device)
+        self.data = torch.zeros(first, 2, num_kv_heads, PAGE, head_dim, dtype=dtype, device=device)
+        self.scales = None
+        if dtype == torch.float8_e4m3fn:
+            if scales is None:
+                ones = torch.ones(num_layers, num_kv_heads, dtype=torch.float32, device=device)
+                scales = (ones, ones.clone())
+            self.scales = tuple(s.to(device=device, dtype=torch.float32).contiguous() for s in scales)
+
+    @property
+    def num_pages(self) -> int:
+        return self.data.shape[0]
+
+    def layer(self, index: int) -> tuple[torch.Tensor, torch.Tensor]:
+        """Views ``[P, H_kv, 128, D]`` of every page's K and V blocks (pages 2 H_kv 128 rows apart)."""
+        return self.data[:, 0], self.data[:, 1]
+
+    def pages(self, index: int) -> torch.Tensor:
+        """Layer ``index``'s page table ``[B, C]``."""
+        return self.tables[index]
+
+    def window_of(self, index: int) -> int:
+        return self.rings[index] * PAGE if self.rings[index] else 0
+
+    def layer_scales(self, index: int) -> tuple[torch.Tensor | None, torch.Tensor | None]:
+        if self.scales is None:
+            return None, None
+        return self.scales[0][index], self.scales[1][index]
+
+    @property
+    def nbytes(self) -> int:
+        return self.data.numel() * self.data.element_size()
+
+    def reset(self) -> None:
+        self.data.zero_()
+
+    def logical(self, index: int, kv: int) -> torch.Tensor:
+        """Layer ``index``'s K (``kv = 0``) or V as a logical ``[B, H_kv, S, D]`` copy (a ring layer's chunks repeat
+        their page: only the window's slots are meaningful)."""
+        pages = self.data[self.tables[index].long(), kv]  # [B, C, H_kv, 128, D]
+        b, c, h, _, d = pages.shape
+        return pages.permute(0, 2, 1, 3, 4).reshape(b, h, c * PAGE, d)
 
 
 @dataclass

@@ -39,11 +39,14 @@ class DraftLayer(nn.Module):
         self._rope_config = config
         self._rope = None
 
-    def rope(self) -> tuple[torch.Tensor, torch.Tensor]:
+    def rope(self, length: int = 0) -> tuple[torch.Tensor, torch.Tensor]:
+        """``cos, sin`` tables with a row for every position below ``length`` (at least the configuration's
+        ``max_position_embeddings``)."""
         dev = self.wqkv.device
-        if self._rope is None or self._rope[0].device != dev:
+        need = max(length, self._rope_config.max_position_embeddings)
+        if self._rope is None or self._rope[0].device != dev or self._rope[0].shape[0] < need:
             inv = rope_inv_freq(self._rope_config).to(dev)
-            pos = torch.arange(self._rope_config.max_position_embeddings, device=dev, dtype=torch.float32)
+            pos = torch.arange(need, device=dev, dtype=torch.float32)
             ang = pos[:, None] * inv[None]
             self._rope = (ang.cos().contiguous(), ang.sin().contiguous())
         return self._rope
@@ -53,7 +56,7 @@ class DraftLayer(nn.Module):
         """``(mlp, a)`` for attention inputs ``x`` and residuals ``residual`` ``[B, T, *]``: the layer output is
         ``a + mlp``, which the caller adds inside its next fused RMSNorm (the draft head's norm); ``mlp`` may be
         split-K :class:`~economize_b200.ops.Partials` that the norm reduces."""
-        cos, sin = self.rope()
+        cos, sin = self.rope(cache.capacity)  # every slot's position has a row
         k_cache, v_cache = cache.layer(0)
         qkv = ops.linear_parts(x, self.wqkv) if self.bqkv is None else ops.linear(x, self.wqkv, self.bqkv)
         q = ops.rope_store(qkv, batch.positions, cos, sin, self.heads, self.kv_heads, self.head_dim, k_cache,

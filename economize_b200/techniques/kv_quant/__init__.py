@@ -172,6 +172,8 @@ class KIVITechnique(Technique):
     def attach(self) -> None:
         if self.model.kv_dtype is not None:
             raise ConfigError("kivi codes a bf16 cache; it cannot be combined with kv_fp8")
+        if self.model.device.type == "cuda" and self.model.config.head_dim != 128:
+            raise ConfigError(f"kivi's CUDA kernels code 128-dimensional heads, not {self.model.config.head_dim}")
         self.model.kv_quantizer = self
 
     def detach(self) -> None:
@@ -182,9 +184,11 @@ class KIVITechnique(Technique):
 
         key = id(cache.data)
         st = self._store.get(key)
-        L, _, B, hkv, S, _ = cache.data.shape
+        if getattr(cache, "paged", False):
+            L, B, hkv, S, dim = cache.num_layers, cache.batch, cache.num_kv_heads, cache.capacity, cache.head_dim
+        else:
+            L, _, B, hkv, S, dim = cache.data.shape
         if st is None or st[0].shape[:4] != (L, B, hkv, S // 128):
-            dim = cache.data.shape[-1]
             st = (torch.zeros(L, B, hkv, S // 128, chunk_bytes(self.config.bits, dim), dtype=torch.uint8,
                               device=cache.data.device),
                   torch.zeros(B, dtype=torch.int32, device=cache.data.device))
@@ -203,7 +207,7 @@ class KIVITechnique(Technique):
 
         data, chunks = self.storage(cache)
         ops.kivi_quantize(cache.data, data, kv_len.to(torch.int32), chunks, self.config.bits, self.config.residual,
-                          max_new)
+                          max_new, pages=cache.tables)
 
 
 @register_technique

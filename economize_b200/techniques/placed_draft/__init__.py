@@ -60,6 +60,8 @@ class PlacedDraftModelTechnique(DraftModelTechnique):
     def __init__(self, config: PlacedDraftModelConfig, model) -> None:
         super(DraftModelTechnique, self).__init__(config, model)
         device = torch.device(config.device)
+        if device.type == "cuda" and device.index is None:  # "cuda": the current device
+            device = torch.device("cuda", torch.cuda.current_device() if torch.cuda.is_available() else 0)
         if device.type == "cuda" and (not torch.cuda.is_available() or device.index >= torch.cuda.device_count()):
             raise ConfigError(f"placed_draft_model: device {config.device} is not available")
         self._draft = [load_draft(config, model).to(device)]

@@ -33,8 +33,9 @@ def test_registries():
 def test_decode_config_checks():
     with pytest.raises(eco.ConfigError):
         eco.DecodeConfig(cycle_length=0)
+    assert eco.DecodeConfig(window_cache=True).window_cache  # ring caches of sliding-window layers
     with pytest.raises(eco.ConfigError):
-        eco.DecodeConfig(window_cache=True)
+        eco.DecodeConfig(prefill_chunk=0)
     cfg = eco.DecodeConfig(cycle_length=7, draft_policy="dynamic_tree", draft_policy_options={"depth": 6})
     assert eco.DecodeConfig.from_dict(cfg.to_dict()) == cfg
     assert hash(cfg) == hash(eco.DecodeConfig.from_dict(json.loads(json.dumps(cfg.to_dict()))))

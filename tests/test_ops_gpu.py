@@ -399,3 +399,27 @@ def test_tree_layout_matches_pointer_doubling(cuda):
         ref = ancestor_bits(parents, 63)
         assert torch.equal(bits.cpu(), ref)
         assert torch.equal(pos.cpu(), (kv_len[:, None] + popcount64(ref) - 1).int())
+
+
+def test_rope_store_reports_positions_and_slots_out_of_range(cuda):
+    """A position past the rotary tables or a slot past the cache is reported in the status word and never read or
+    written (the tables of a model cover its cache's capacity, so the engine never hits this)."""
+    g = torch.Generator(device=cuda).manual_seed(9)
+    B, T, H, Hkv, S, D = 1, 4, 4, 2, 128, 128
+    qkv = torch.randn(B, T, (H + 2 * Hkv) * D, device=cuda, generator=g).bfloat16()
+    cos = torch.randn(64, D // 2, device=cuda, generator=g)
+    sin = torch.randn(64, D // 2, device=cuda, generator=g)
+    k = torch.zeros(B, Hkv, S, D, device=cuda, dtype=torch.bfloat16)
+    v = torch.zeros_like(k)
+    ops.require().status(0)  # start clean
+    pos = torch.tensor([[10, 63, 64, 500]], dtype=torch.int32, device=cuda)
+    q = ops.rope_store(qkv, pos, cos, sin, H, Hkv, D, k, v, torch.tensor([0], dtype=torch.int32, device=cuda),
+                       torch.tensor([T], dtype=torch.int32, device=cuda))
+    torch.cuda.synchronize()
+    assert ops.require().status(0) & 32 and torch.isfinite(q.float()).all()
+    kv_len = torch.tensor([S - 2], dtype=torch.int32, device=cuda)  # the last two tokens fall past the cache
+    ops.rope_store(qkv, pos.clamp(max=63), cos, sin, H, Hkv, D, k, v, kv_len,
+                   torch.tensor([T], dtype=torch.int32, device=cuda))
+    torch.cuda.synchronize()
+    assert ops.require().status(0) & 32
+    assert k[0, :, S - 2:].abs().sum() > 0  # the two slots inside the cache were written

@@ -92,3 +92,38 @@ def test_lookahead_refuses_trees_beyond_the_pass():
 
     with pytest.raises(ConfigError, match="nodes"):
         LookaheadConfig(window=15, ngram=5, guesses=15)
+
+
+def test_suffix_index_orders_suffixes_and_counts_continuations(tmp_path):
+    import numpy as np
+
+    from economize_b200.techniques.retrieval import SuffixIndex, suffix_array
+
+    toks = np.array([3, 1, 2, 3, 1, 2, 4, -1, 3, 1, 5, -1], dtype=np.int64)
+    sa = suffix_array(toks, depth=64)
+    keys = [tuple(toks[i:i + 6].tolist()) for i in sa]
+    assert keys == sorted(keys)  # sorted by their first tokens (separators lowest)
+    idx = SuffixIndex.build([[3, 1, 2, 3, 1, 2, 4], [3, 1, 5]])
+    lo, hi = idx.find([3, 1])
+    assert hi - lo == 3
+    tokens, parents = idx.draft_tree([9, 3, 1], budget=4, max_depth=2, branch=2, min_match=1)
+    assert tokens[0] == 2 and parents[0] == -1  # "3 1" is followed by 2 twice and by 5 once
+    idx.save(tmp_path / "store")
+    again = SuffixIndex.load(tmp_path / "store", mmap=True)
+    assert again.draft_tree([9, 3, 1], 4, 2, 2, 1) == (tokens, parents)
+
+
+def test_rest_with_a_persistent_datastore_and_cli(tmp_path):
+    import numpy as np
+
+    from economize_b200.techniques.retrieval.__main__ import main
+
+    model = tiny_model()
+    p = _repetitive_prompt()
+    ref = reference_greedy(model, p, 16)
+    flat = torch.cat([p, ref]).numpy().astype(np.uint32)
+    flat.tofile(tmp_path / "corpus.bin")
+    main(["build", str(tmp_path / "store"), "--tokens", str(tmp_path / "corpus.bin"), "--depth", "32"])
+    eff = eco.apply(model, RestConfig(datastore=str(tmp_path / "store")))
+    out = eff.decode(p, 16)
+    assert torch.equal(out.tokens, ref) and out.mean_accepted > 1.0
