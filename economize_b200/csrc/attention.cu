@@ -323,6 +323,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   }
   const int c0 = (g0 + split) * chunks_per_split;
   const int c1 = min(n_chunks, c0 + chunks_per_split);
+  if (!index_ok(base >= 0 && nn >= 0 && base <= S, tid == 0 ? status : nullptr)) return;  // bounds-checked builds
 
   const int q_chunks = (!FP8 && kivi != nullptr) ? kivi_chunks[b] : 0;  // chunks [0, q_chunks) are KIVI-coded
   auto issue_kv = [&](int c, int s) {
@@ -672,7 +673,8 @@ __global__ void __launch_bounds__(128) attn_merge_tail_kernel(
     const uint8_t* __restrict__ k_cache, const uint8_t* __restrict__ v_cache, const int* __restrict__ kv_len,
     const int* __restrict__ n_new, const int64_t* __restrict__ mask, int S, float scale_log2, int q_offset,
     int tail_w, const float* __restrict__ k_scale, const float* __restrict__ v_scale,
-    const uint32_t* __restrict__ keep, float softcap, const float* __restrict__ sinks, KVPages pages) {
+    const uint32_t* __restrict__ keep, float softcap, const float* __restrict__ sinks, KVPages pages,
+    unsigned* status) {
   __shared__ int s_row[4][kTailKeysMax];    // cache rows of this warp's tail keys, in position order
   __shared__ float s_sc[4][kTailKeysMax];   // their scaled scores
   pdl_trigger();
@@ -721,6 +723,11 @@ __global__ void __launch_bounds__(128) attn_merge_tail_kernel(
     n_keys += __popc(ballot);
   }
   __syncwarp();
+  if constexpr (kCheckedBuild) {  // tail slots come from kv_len / n_new on the device
+    bool bad = false;
+    for (int i = lane; i < n_keys; i += 32) bad |= !(s_row[wid][i] >= 0 && s_row[wid][i] < S);
+    if (!index_ok(!__any_sync(0xffffffffu, bad), lane == 0 ? status : nullptr)) n_keys = 0;
+  }
 
   // scores, batches of kTailBatch keys whose K loads are in flight together
   float mx = -INFINITY;
@@ -906,6 +913,7 @@ __global__ void __launch_bounds__(128) kivi_quantize_kernel(const bf16* __restri
   const int layer = blockIdx.x, bh = blockIdx.y, b = bh / Hkv;
   const int c = chunks[b] + static_cast<int>(blockIdx.z);
   if ((c + 1) * kKeys + residual > kv_len[b]) return;
+  if (!index_ok(c >= 0 && (c + 1) * kKeys <= S, nullptr)) return;
   __shared__ uint8_t codes[kKeys][kDim + 4];
   const int tid = threadIdx.x;
   const float levels = static_cast<float>((1 << bits) - 1);
@@ -1050,7 +1058,7 @@ int launch_attention(const void* q, const CUtensorMap* tm_k, const CUtensorMap* 
                static_cast<const float*>(ws_ml), static_cast<bf16*>(out), T, H, Hkv, plan.m_tiles, plan.splits,
                lse_out, static_cast<const bf16*>(q), static_cast<const uint8_t*>(k_cache),
                static_cast<const uint8_t*>(v_cache), kv_len, n_new, mask, S, sl2, q_offset, tail_w, k_scale, v_scale,
-               keep, opts.softcap, opts.sinks, pages);
+               keep, opts.softcap, opts.sinks, pages, status);
   } else if (plan.splits > 1) {
     auto merge = D == 64 ? attn_merge_kernel<64> : D == 256 ? attn_merge_kernel<256> : attn_merge_kernel<128>;
     launch_pdl(merge, mgrid, dim3(128), 0, stream, static_cast<const float*>(ws_o),

@@ -269,6 +269,24 @@ inline cudaError_t launch_pdl(void (*kernel)(KArgs...), dim3 grid, dim3 block, s
   return cudaLaunchKernelEx(&cfg, kernel, static_cast<KArgs>(args)...);
 }
 
+// ---- bounds-checked builds ---------------------------------------------------------------------------------------
+// Built with -DECZ_CHECK (ECZ_CHECK=1 python setup.py build_ext --inplace: the module economize_b200._C_check, loaded
+// when the environment has ECZ_CHECK=1), kernels check the indices they read from device memory before those
+// address memory; a bad one sets kStatusBadIndex in the device status word and the access is skipped. Nothing
+// traps, so the context stays usable and the host reads the flag (ops.require().status). Regular builds compile
+// the checks away.
+#ifdef ECZ_CHECK
+constexpr bool kCheckedBuild = true;
+#else
+constexpr bool kCheckedBuild = false;
+#endif
+
+__device__ __forceinline__ bool index_ok(bool in_range, unsigned* status) {
+  if (!kCheckedBuild || in_range) return true;
+  if (status != nullptr) atomicOr(status, kStatusBadIndex);
+  return false;
+}
+
 // ---- KV cache addressing ----------------------------------------------------------------------------------------
 // Where the K (or V) row of (sequence b, KV head kvh, logical slot s) lives. Contiguous caches [B, Hkv, S, D]: row
 // (b Hkv + kvh) S + s. Paged caches: logical chunk s / 128 of sequence b sits in page table[b * max_chunks + s / 128]

@@ -4,11 +4,13 @@ The extension is built in-tree (``python setup.py build_ext --inplace``, or ``__
 tensors always go to it: :func:`require` raises :class:`~economize_b200.errors.KernelUnavailableError` when it is
 missing instead of falling back to PyTorch, so a GPU run can never pass on a silent eager path. CPU tensors use the
 PyTorch implementations in :mod:`economize_b200.ops.reference` (the numerics oracle of the kernel tests).
+With ``ECZ_CHECK=1`` in the environment the bounds-checked build ``economize_b200._C_check`` is loaded instead.
 """
 
 from __future__ import annotations
 
 import importlib
+import os
 from types import ModuleType
 
 from ..errors import KernelUnavailableError
@@ -26,10 +28,15 @@ def _load() -> ModuleType | None:
     try:
         import torch  # noqa: F401  (the extension links against libtorch)
 
-        _module = importlib.import_module("economize_b200._C")
+        _module = importlib.import_module(module_name())
     except Exception as err:  # ImportError, or an undefined symbol of a stale build
         _error = f"{type(err).__name__}: {err}"
     return _module
+
+
+def module_name() -> str:
+    """``economize_b200._C``, or the bounds-checked build ``economize_b200._C_check`` when ``ECZ_CHECK=1``."""
+    return "economize_b200._C_check" if os.environ.get("ECZ_CHECK") == "1" else "economize_b200._C"
 
 
 def available() -> bool:
@@ -46,5 +53,5 @@ def require() -> ModuleType:
     """The extension module; raises when it is missing (a CUDA tensor must never take a fallback path)."""
     module = _load()
     if module is None:
-        raise KernelUnavailableError(f"economize_b200._C is not built or failed to load ({_error})")
+        raise KernelUnavailableError(f"{module_name()} is not built or failed to load ({_error})")
     return module

@@ -13,7 +13,8 @@ drafter's speculation; Gloo on the CPU). Per round:
     drafter  on a hit the next spine is ready at once (its K/V are moved to their slots by the compaction kernel);
              on a miss it drafts after y
 
-The output equals the target's greedy decoding. Batch size one: SSD trades drafter work for latency.
+The output equals the target's greedy decoding, or with ``temperature > 0`` is distributed as the target's own
+sampling (speculative sampling verification). Batch size one: SSD trades drafter work for latency.
 """
 
 from __future__ import annotations
@@ -34,24 +35,44 @@ __all__ = ["AsyncSpeculativeDecoder", "SSDConfig", "SSDResult", "ssd_generate"]
 @dataclass(frozen=True)
 class SSDConfig:
     """``draft_length`` ``k`` drafts per round; ``fanout`` guesses per outcome depth; ``mode``: ``"async"``
-    (speculate while the target verifies) or ``"sync"`` (draft after every outcome); ``temperature`` must be 0
-    (greedy verification)."""
+    (speculate while the target verifies) or ``"sync"`` (draft after every outcome). ``temperature`` 0 verifies
+    greedily; above 0 the target samples losslessly from its (``top_p``-filtered) distribution by speculative
+    sampling: the drafter's greedy drafts are point masses ``q``, so draft ``d`` is kept with probability ``p(d)``
+    and a rejection draws from ``p`` without ``d`` renormalised, the output distribution being the target's own.
+    ``seed`` starts the target's sampling generator afresh for every generation."""
 
     draft_length: int = 4
     fanout: int = 2
     mode: str = "async"
     temperature: float = 0.0
+    top_p: float = 1.0
+    seed: int = 0
 
     def __post_init__(self) -> None:
         check_positive("draft_length", self.draft_length)
         check_positive("fanout", self.fanout)
         check_choice("mode", self.mode, ("async", "sync"))
-        if self.temperature != 0.0:
-            raise ConfigError("this SSD verifies greedily (temperature=0)")
+        if self.temperature < 0.0 or not 0.0 < self.top_p <= 1.0:
+            raise ConfigError(f"SSD needs temperature >= 0 and 0 < top_p <= 1, got {self.temperature}, {self.top_p}")
         k, g = self.draft_length, (self.draft_length + 1) * self.fanout
         if (k + 1) + g * (k + 1) > 64:
             raise ConfigError("(k + 1) (1 + (k + 1) fanout) must not exceed 64 (the speculation tree's ancestor "
                               "bits are one int64 per node)")
+
+    @property
+    def sampling(self) -> bool:
+        return self.temperature > 0.0
+
+
+def _probs(logits: torch.Tensor, config: SSDConfig) -> torch.Tensor:
+    """The target's sampling distribution ``[..., V]``: softmax at ``temperature``, then nucleus ``top_p``."""
+    p = torch.softmax(logits.float() / config.temperature, -1)
+    if config.top_p < 1.0:
+        sorted_p, order = p.sort(-1, descending=True)
+        keep = sorted_p.cumsum(-1) - sorted_p < config.top_p  # the smallest prefix whose mass reaches top_p
+        p = torch.zeros_like(p).scatter_(-1, order, sorted_p * keep)
+        p = p / p.sum(-1, keepdim=True)
+    return p
 
 
 @dataclass
@@ -210,7 +231,13 @@ def _target_loop(model, prompt, max_new, config, link: _Link, capacity: int) -> 
     if prompt.numel() > 1:
         _prefill(model, prompt[:-1], cache)
     last = _chain_pass(model, prompt[-1:], prompt.numel() - 1, cache)[-1]
-    root = int(ops.argmax(model.logits(last[None]))[0])
+    gen = torch.Generator(device=dev)
+    gen.manual_seed(config.seed)
+    if config.sampling:
+        u = torch.rand(1, generator=gen, device=dev)
+        root = int(ops.sample(_probs(model.logits(last[None]), config), u)[0])
+    else:
+        root = int(ops.argmax(model.logits(last[None]))[0])
     out = [root]
     n = prompt.numel() + 1  # committed tokens; the last (root) sits at position n - 1 without K/V yet
     result = SSDResult(torch.empty(0))
@@ -221,10 +248,18 @@ def _target_loop(model, prompt, max_new, config, link: _Link, capacity: int) -> 
         link.recv(spine)
         chain = torch.cat([torch.tensor([out[-1]], device=dev), spine])
         hidden = _chain_pass(model, chain, n - 1, cache)
-        pred = model.greedy(hidden)  # [k + 1]
-        ok = (pred[:-1] == spine).int().cumprod(0)
-        a = ok.sum()
-        y = pred[a]
+        if config.sampling:  # speculative sampling with point-mass drafts (lossless for any drafter)
+            p = _probs(model.logits(hidden), config)[None]  # [1, k + 1, V]
+            q = torch.zeros(1, k, p.shape[-1], dtype=p.dtype, device=dev)
+            q[0, torch.arange(k, device=dev), spine] = 1.0
+            n_acc, drawn = ops.rejection(p, q, spine[None], torch.rand(1, k, generator=gen, device=dev),
+                                         torch.rand(1, generator=gen, device=dev))
+            a, y = n_acc[0], drawn[0, n_acc[0]]
+        else:
+            pred = model.greedy(hidden)  # [k + 1]
+            ok = (pred[:-1] == spine).int().cumprod(0)
+            a = ok.sum()
+            y = pred[a]
         a_i, y_i = int(a), int(y)  # waits for the target's pass only
         committed = spine[:a_i].tolist() + [y_i]
         out.extend(committed)

@@ -18,12 +18,18 @@ if os.path.exists(HOST_CXX):
     os.environ["LDSHARED"] = HOST_CXX + " -shared"
 CSRC = os.path.join(HERE, "economize_b200", "csrc")
 
+# ECZ_CHECK=1 builds the bounds-checked variant economize_b200._C_check (kernels check the indices they read from
+# device memory and report bad ones in the status word); build it into its own temp folder so the two variants'
+# objects do not overwrite each other: ECZ_CHECK=1 python setup.py build_ext --inplace --build-temp build/check
+CHECKED = os.environ.get("ECZ_CHECK") == "1"
+
 NVCC_FLAGS = [
     "-gencode", "arch=compute_100a,code=sm_100a",
     *(["-ccbin", HOST_CXX] if os.path.exists(HOST_CXX) else []),
     "-O3", "-lineinfo", "-std=c++17",
     "--expt-relaxed-constexpr",
     "-Xptxas", "-v" if os.environ.get("ECZ_PTXAS_VERBOSE") else "-O3",
+    *(["-DECZ_CHECK"] if CHECKED else []),
 ]
 
 sources = sorted(glob.glob(os.path.join(CSRC, "*.cu"))) + sorted(glob.glob(os.path.join(CSRC, "*.cpp")))
@@ -35,10 +41,11 @@ setup(
     packages=find_packages(include=["economize_b200", "economize_b200.*"]),
     ext_modules=[
         CUDAExtension(
-            name="economize_b200._C",
+            name="economize_b200._C_check" if CHECKED else "economize_b200._C",
             sources=sources,
             include_dirs=[CSRC],
-            extra_compile_args={"cxx": ["-O3", "-std=c++17"], "nvcc": NVCC_FLAGS},
+            extra_compile_args={"cxx": ["-O3", "-std=c++17", *(["-DECZ_CHECK"] if CHECKED else [])],
+                                "nvcc": NVCC_FLAGS},
         )
     ],
     cmdclass={"build_ext": BuildExtension.with_options(use_ninja=True)},

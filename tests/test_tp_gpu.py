@@ -89,7 +89,7 @@ def _worker(rank, world, port, queue):
         sp.check()
         sp.close()
         # TP decoding, NCCL and fused: greedy-valid tokens identical on all ranks
-        cfg = tiny_llama(hidden_size=1024, num_heads=8, num_kv_heads=4, head_dim=128, intermediate_size=2048,
+        cfg = tiny_llama(hidden_size=1024, num_heads=8, num_kv_heads=8, head_dim=128, intermediate_size=2048,
                          num_layers=3)
         prompts = [torch.randint(0, 1024, (n,), generator=torch.Generator().manual_seed(n)).to(dev) for n in (9, 30)]
         single = init_weights(CausalLM(cfg, torch.bfloat16, dev), seed=0)
@@ -139,13 +139,14 @@ def _worker(rank, world, port, queue):
     dist.destroy_process_group()
 
 
-def test_tp2_fused_collectives():
-    if torch.cuda.device_count() < 2:
-        pytest.skip("needs 2 GPUs")
+@pytest.mark.parametrize("world", [2, 4, 8])
+def test_tp_fused_collectives(world):
+    if torch.cuda.device_count() < world:
+        pytest.skip(f"needs {world} GPUs")
     ctx = mp.get_context("spawn")
     queue = ctx.Queue()
     port = _port()
-    procs = [ctx.Process(target=_worker, args=(r, 2, port, queue), daemon=True) for r in range(2)]
+    procs = [ctx.Process(target=_worker, args=(r, world, port, queue), daemon=True) for r in range(world)]
     for p in procs:
         p.start()
     try:
