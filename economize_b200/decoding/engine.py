@@ -401,7 +401,8 @@ class SpecEngine:
     def _run_cycles(self, st: _State, max_new: int, stop_tokens: list[int] | None) -> None:
         # drafters that search host-side structures (retrieval, suffix trees) synchronise with the host every cycle
         use_graph = self.config.cuda_graphs and self.model.device.type == "cuda" and \
-            getattr(self.drafter, "graph_safe", True) and self.acceptance is None
+            getattr(self.drafter, "graph_safe", True) and self.acceptance is None and \
+            getattr(self.model, "placement", None) is None  # a graph belongs to one device
         key = (st.batch, st.capacity, st.out_cap)
         remaining = max_new - 1  # the prefill produced the first token
         per_cycle = self.tokens_per_cycle
@@ -497,7 +498,7 @@ class SpecEngine:
             after(tokens, self.last_pred)
         if self.acceptance is not None:  # Sequoia rate measurement: one host synchronization per cycle
             record_cycle(self.acceptance, self.static_tree, self._plan(dev), tokens, path, n_acc, out)
-        ops.kv_compact(st.cache.data, st.kv_len, path, n_acc, st.cache.tables)
+        st.cache.compact(st.kv_len, path, n_acc)
         # ---- commit ----
         active = st.n_out < st.max_new
         width = depth + 1

@@ -25,7 +25,7 @@ from torch import nn
 
 from .. import ops
 from ..errors import ConfigError
-from ..runtime.cache import KVCache, PagedKVCache, StepBatch
+from ..runtime.cache import KVCache, PagedKVCache, SplitKVCache, StepBatch
 from .config import ModelConfig, rope_inv_freq
 
 __all__ = ["CausalLM", "DecoderLayer", "init_weights"]
@@ -78,6 +78,10 @@ class CausalLM(nn.Module):
         device: Where the parameters live.
     """
 
+    #: class-level defaults, so views built without ``__init__`` (``techniques/_self_draft.py:layer_view``) have them
+    placement = None
+    _rope_local = None
+
     def __init__(self, config: ModelConfig, dtype: torch.dtype = torch.bfloat16,
                  device: torch.device | str | None = None) -> None:
         super().__init__()
@@ -105,6 +109,8 @@ class CausalLM(nn.Module):
         #: before each query in position order (ops.attention's exact tail), so greedy speculative decoding with
         #: trees up to this deep reproduces plain greedy decoding bit for bit; 0 turns it off
         self.exact_tail = 16
+        #: device of every decoder layer under pipeline placement (economize_b200.parallel.pipeline), else None
+        self.placement: list[torch.device] | None = None
         #: tensor-parallel group (set by economize_b200.parallel.tp.shard_model) and this rank's shard sizes
         self.tp = None
         self.local = dict(num_heads=config.num_heads, num_kv_heads=config.num_kv_heads,
@@ -157,6 +163,20 @@ class CausalLM(nn.Module):
         sliding-window layers get ring tables of their window (plus ``reserve`` slots a pass may write)."""
         c = self.config
         dtype = self.kv_dtype or self.dtype
+        if self.placement is not None:  # one cache per pipeline stage, on the stage's device
+            if paged or rings:
+                raise ConfigError("pipeline placement keeps contiguous caches (no paged or ring caches)")
+            parts, start = [], 0
+            while start < c.num_layers:
+                dev = self.placement[start]
+                stop = start
+                while stop < c.num_layers and self.placement[stop] == dev:
+                    stop += 1
+                scales = None if self.kv_scales is None else tuple(t[start:stop].to(dev) for t in self.kv_scales)
+                parts.append((range(start, stop), KVCache(stop - start, batch, self.local["num_kv_heads"], capacity,
+                                                          c.head_dim, dtype, dev, scales)))
+                start = stop
+            return SplitKVCache(parts)
         if paged or rings:
             windows = [c.window_of(i) for i in range(c.num_layers)] if rings else None
             return PagedKVCache(c.num_layers, batch, self.local["num_kv_heads"], capacity, c.head_dim, dtype,
@@ -211,8 +231,11 @@ class CausalLM(nn.Module):
         depth = self.depth_policy if self.depth_policy is not None and self.depth_policy.acts(batch) else None
         if depth is not None:
             depth.begin_pass(batch, h)
+        staged = self._stage(batch, cos, sin) if self.placement is not None else None
         for i in todo:
             layer = self.layers[i]
+            if staged is not None:  # pipeline placement: the stream moves to the layer's device
+                h, resid, partial, batch, cos, sin = staged(i, h, resid, partial)
             gated = depth is not None and depth.gates(i)
             x_in = None
             # a layer view may skip a sublayer (self-drafting): the pending branch output is added at the next norm
@@ -235,6 +258,9 @@ class CausalLM(nn.Module):
                 # dynamic depth: the policy decides, per token, how the layer's output enters the stream
                 out = resid + self._materialize(h, partial)
                 h, resid, partial = depth.combine(i, x_in, out, batch), None, False
+        if staged is not None:  # back to the home device (embedding, final norm, LM head, the engine's state)
+            h, resid, partial, batch, cos, sin = staged(None, h, resid, partial)
+            aux = {k: v.to(self.device) for k, v in aux.items()}
         h, partial = self._scale_branch(h, partial)
         out, resid = self._norm(h, self.norm, resid, partial)
         if c.num_layers in capture:
@@ -244,6 +270,24 @@ class CausalLM(nn.Module):
         if -2 in capture:
             aux[-2] = resid
         return out, aux
+
+    def _stage(self, batch: StepBatch, cos: torch.Tensor, sin: torch.Tensor):
+        """Pipeline placement: a function ``(layer or None, h, resid, partial)`` that moves the residual stream, the
+        pass's batch description and the rotary tables to the layer's device (``None``: the home device), with the
+        per-device copies of the batch and tables made once per pass."""
+        copies: dict[torch.device, tuple[StepBatch, torch.Tensor, torch.Tensor]] = {}
+
+        def move(i, h, resid, partial):
+            dev = self.device if i is None else self.placement[i]
+            if dev not in copies:
+                copies[dev] = (batch.to(dev), cos.to(dev), sin.to(dev))
+            if h.device != dev:
+                h = self._materialize(h, partial).to(dev)
+                partial = False
+                resid = None if resid is None else resid.to(dev)
+            return (h, resid, partial) + copies[dev]
+
+        return move
 
     def _scale_branch(self, h, partial: bool):
         """A branch output times Granite's residual multiplier before it joins the residual stream (a no-op for
@@ -264,8 +308,11 @@ class CausalLM(nn.Module):
         h = self.embed_tokens(tokens) if hidden is None else hidden
         aux: dict[int, torch.Tensor] = {}
         sandwich = c.sandwich_norm
+        staged = self._stage(batch, cos, sin) if self.placement is not None else None
         for i in (layers if layers is not None else range(c.num_layers)):
             layer = self.layers[i]
+            if staged is not None:
+                h, _, _, batch, cos, sin = staged(i, h, None, False)
             if i in capture:
                 aux[i] = h
             x = ops.rmsnorm(h, layer.attn_norm, eps)[0] if sandwich else h
@@ -274,6 +321,9 @@ class CausalLM(nn.Module):
             x = ops.rmsnorm(h, layer.mlp_norm, eps)[0] if sandwich else h
             m = self._materialize(self._mlp(layer, x, i), True)
             h = h + ops.rmsnorm(m, layer.mlp_post_norm if sandwich else layer.mlp_norm, eps)[0]
+        if staged is not None:
+            h, _, _, batch, cos, sin = staged(None, h, None, False)
+            aux = {k: v.to(self.device) for k, v in aux.items()}
         out = ops.rmsnorm(h, self.norm, eps)[0]
         if c.num_layers in capture or -2 in capture:
             aux[c.num_layers] = aux[-2] = h
@@ -287,7 +337,8 @@ class CausalLM(nn.Module):
         of a dense model without per-token layer policies, views that skip sublayers, or calibration hooks."""
         tp = self.tp
         sp = getattr(tp, "sp", None) if tp is not None else None
-        if sp is None or layers is not None or hidden is not None or not sp.fits(tokens.numel()):
+        if sp is None or layers is not None or hidden is not None or not sp.fits(tokens.numel()) or \
+                self.placement is not None:
             return False
         c = self.config
         if c.is_moe or self.observer is not None or self.depth_policy is not None or c.post_norm or \
@@ -422,7 +473,7 @@ class CausalLM(nn.Module):
         """A projection whose consumer is one of the engine's fused elementwise kernels: without tensor
         parallelism the GEMM may hand over its split-K partials (:class:`~economize_b200.ops.Partials`), which the
         consumer reduces while reading them."""
-        if self.tp is None or self.tp.size == 1:
+        if (self.tp is None or self.tp.size == 1) and self.placement is None:
             return ops.linear_parts(x, weight)
         return ops.linear(x, weight)
 

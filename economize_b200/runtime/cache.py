@@ -16,7 +16,7 @@ from dataclasses import dataclass
 
 import torch
 
-__all__ = ["KVCache", "PAGE", "PagedKVCache", "StepBatch", "ring_pages"]
+__all__ = ["KVCache", "PAGE", "PagedKVCache", "SplitKVCache", "StepBatch", "ring_pages"]
 
 #: slots per page of a paged cache (one key tile of the attention kernel)
 PAGE = 128
@@ -59,6 +59,12 @@ class KVCache:
     def pages(self, index: int) -> None:
         """A contiguous cache has no page table."""
         return None
+
+    def compact(self, kv_len: torch.Tensor, path: torch.Tensor, n_acc: torch.Tensor) -> None:
+        """Move every row's accepted tree path to consecutive slots in every layer (the compaction kernel)."""
+        from .. import ops
+
+        ops.kv_compact(self.data, kv_len, path, n_acc)
 
     tables = None
     paged = False
@@ -127,6 +133,11 @@ class PagedKVCache:
         """Layer ``index``'s page table ``[B, C]``."""
         return self.tables[index]
 
+    def compact(self, kv_len: torch.Tensor, path: torch.Tensor, n_acc: torch.Tensor) -> None:
+        from .. import ops
+
+        ops.kv_compact(self.data, kv_len, path, n_acc, self.tables)
+
     def window_of(self, index: int) -> int:
         return self.rings[index] * PAGE if self.rings[index] else 0
 
@@ -176,6 +187,12 @@ class StepBatch:
     #: slot, without the exact tail of decode passes, so a chunked prefill matches a whole one
     prompt: bool = False
 
+    def to(self, device: torch.device | str) -> StepBatch:
+        """This batch with its tensors on ``device``."""
+        move = (lambda t: None if t is None else t.to(device))
+        return StepBatch(move(self.kv_len), move(self.n_new), move(self.positions), move(self.mask), self.q_offset,
+                         self.is_prefill, self.prompt)
+
     @staticmethod
     def prefill(lengths: torch.Tensor, width: int) -> StepBatch:
         """A causal pass over prompts of ``lengths`` padded to ``width`` tokens, starting at slot 0."""
@@ -184,3 +201,49 @@ class StepBatch:
         positions = torch.arange(width, device=device, dtype=torch.int32).expand(batch, width).contiguous()
         return StepBatch(torch.zeros(batch, dtype=torch.int32, device=device), lengths.to(torch.int32), positions,
                          is_prefill=True, prompt=True)
+
+
+class SplitKVCache:
+    """The cache of a model whose layers are split over devices (pipeline placement): one contiguous
+    :class:`KVCache` per stage, on the stage's device, holding that stage's layers."""
+
+    paged = False
+    tables = None
+
+    def __init__(self, parts: list[tuple[range, KVCache]]) -> None:
+        self.parts = parts
+        self._of: dict[int, tuple[int, KVCache]] = {}
+        for layers, part in parts:
+            for i in layers:
+                self._of[i] = (i - layers.start, part)
+        first = parts[0][1]
+        self.num_layers = sum(len(r) for r, _ in parts)
+        self.batch, self.capacity = first.batch, first.capacity
+
+    def layer(self, index: int) -> tuple[torch.Tensor, torch.Tensor]:
+        local, part = self._of[index]
+        return part.layer(local)
+
+    def layer_scales(self, index: int) -> tuple[torch.Tensor | None, torch.Tensor | None]:
+        local, part = self._of[index]
+        return part.layer_scales(local)
+
+    def pages(self, index: int) -> None:
+        return None
+
+    @property
+    def data(self) -> torch.Tensor:
+        raise AttributeError("a split cache has one tensor per stage (see parts)")
+
+    @property
+    def nbytes(self) -> int:
+        return sum(part.nbytes for _, part in self.parts)
+
+    def reset(self) -> None:
+        for _, part in self.parts:
+            part.reset()
+
+    def compact(self, kv_len: torch.Tensor, path: torch.Tensor, n_acc: torch.Tensor) -> None:
+        for _, part in self.parts:
+            dev = part.data.device
+            part.compact(kv_len.to(dev), path.to(dev), n_acc.to(dev))

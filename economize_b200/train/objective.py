@@ -176,18 +176,35 @@ class MedusaCE(Objective):
         return loss, metrics
 
 
+def dense_linear(x: torch.Tensor, w, b: torch.Tensor | None = None) -> torch.Tensor:
+    """``x @ w.T (+ b)`` with autograd for a tensor, a quantized weight (dequantized) or a LoRA-wrapped one (base
+    product plus the trainable low-rank update)."""
+    import torch.nn.functional as F
+
+    from ..ops.lora import LoRAWeight
+
+    if isinstance(w, LoRAWeight):
+        y = dense_linear(x, w.base) + w.delta(x).to(x.dtype)
+        return y if b is None else y + b
+    if not isinstance(w, torch.Tensor):
+        w = w.dequantize(x.dtype)
+    return F.linear(x, w, b)
+
+
 def torch_block(layer, h: torch.Tensor, config, cos: torch.Tensor, sin: torch.Tensor) -> torch.Tensor:
     """A pre-norm decoder block in plain PyTorch (autograd, causal attention over the whole row): the residual
-    stream ``h [B, S, H]`` in, the block's output stream out. Used to train technique-owned blocks."""
+    stream ``h [B, S, H]`` in, the block's output stream out. Used to train technique-owned blocks and adapters."""
     import torch.nn.functional as F
 
     from ..ops.reference import rmsnorm
+
+    lin = dense_linear
 
     eps = config.rms_norm_eps
     batch, length, _ = h.shape
     heads, kv_heads, hd = config.num_heads, config.num_kv_heads, config.head_dim
     x = rmsnorm(h, layer.attn_norm, eps)[0]
-    q, k, v = F.linear(x, layer.wqkv, layer.bqkv).split([heads * hd, kv_heads * hd, kv_heads * hd], -1)
+    q, k, v = lin(x, layer.wqkv, layer.bqkv).split([heads * hd, kv_heads * hd, kv_heads * hd], -1)
     q = q.reshape(batch, length, heads, hd)
     k = k.reshape(batch, length, kv_heads, hd)
     if layer.q_norm is not None:
@@ -203,10 +220,38 @@ def torch_block(layer, h: torch.Tensor, config, cos: torch.Tensor, sin: torch.Te
     group = heads // kv_heads
     o = F.scaled_dot_product_attention(q, k.repeat_interleave(group, 1), v.repeat_interleave(group, 1),
                                        is_causal=True)
-    h = h + F.linear(o.transpose(1, 2).reshape(batch, length, heads * hd), layer.wo)
+    h = h + lin(o.transpose(1, 2).reshape(batch, length, heads * hd), layer.wo)
     x = rmsnorm(h, layer.mlp_norm, eps)[0]
-    g, u = F.linear(x, layer.w_gate_up).chunk(2, -1)
-    return h + F.linear(F.silu(g) * u, layer.w_down)
+    g, u = lin(x, layer.w_gate_up).chunk(2, -1)
+    return h + lin(F.silu(g) * u, layer.w_down)
+
+
+@OBJECTIVES.register("recovery_ce")
+class RecoveryCE(Objective):
+    """Next-token cross-entropy of a pruned target through its recovery adapters (LLM-Pruner's recovery stage;
+    economize ``techniques/width_prune/recovery.py``): the whole model runs in plain PyTorch with autograd."""
+
+    def __init__(self, model) -> None:
+        super().__init__(model)
+        self.tech = next(t for t in model.techniques.values() if getattr(t, "recovery", None) is not None)
+
+    def parameters(self) -> list[torch.nn.Parameter]:
+        return list(self.tech.recovery.parameters())
+
+    def loss(self, tokens: torch.Tensor) -> tuple[torch.Tensor, dict[str, float]]:
+        import torch.nn.functional as F
+
+        from ..ops.reference import rmsnorm
+
+        target = self.model.model
+        c = target.config
+        cos, sin = target.rope_tables(tokens.shape[1])
+        h = target.embed_tokens(tokens).float()
+        for layer in target.layers:
+            h = torch_block(layer, h, c, cos, sin)
+        logits = F.linear(rmsnorm(h, target.norm.float(), c.rms_norm_eps)[0], target.head_weight.float())
+        loss = F.cross_entropy(logits[:, :-1].reshape(-1, logits.shape[-1]).float(), tokens[:, 1:].reshape(-1))
+        return loss, {"loss": float(loss.detach())}
 
 
 @OBJECTIVES.register("kangaroo_distill")
