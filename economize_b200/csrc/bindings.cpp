@@ -408,7 +408,7 @@ Tensor attention(Tensor q, Tensor k_cache, Tensor v_cache, Tensor kv_len, Tensor
   return out;
 }
 
-Tensor glu_act(Tensor gu, int64_t act) {
+Tensor glu_act(Tensor gu, int64_t act, double limit) {
   CHECK_CUDA(gu);
   c10::cuda::CUDAGuard guard(gu.device());
   gu = gu.contiguous();
@@ -421,12 +421,12 @@ Tensor glu_act(Tensor gu, int64_t act) {
   auto out = at::empty(shape, gu.options().dtype(at::kBFloat16));
   const int rc = ecz::launch_glu(splits ? nullptr : gu.data_ptr(), out.data_ptr(), rows, F2 / 2,
                                  at::cuda::getCurrentCUDAStream(), splits ? gu.data_ptr<float>() : nullptr, splits,
-                                 static_cast<int>(act));
-  TORCH_CHECK(rc == 0, "glu: width must be a multiple of 16 and act 0 (SiLU) or 1 (GELU tanh)");
+                                 static_cast<int>(act), static_cast<float>(limit));
+  TORCH_CHECK(rc == 0, "glu: width must be a multiple of 16 and act 0 (SiLU), 1 (GELU tanh) or 2 (clamped SwiGLU)");
   return out;
 }
 
-Tensor silu_mul(Tensor gu) { return glu_act(gu, 0); }
+Tensor silu_mul(Tensor gu) { return glu_act(gu, 0, 0.0); }
 
 Tensor linear_bf16(Tensor x, Tensor w) {
   CHECK_CUDA(x);
@@ -1436,7 +1436,8 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
         py::arg("k_cache"), py::arg("kv_len"), py::arg("n_new"), py::arg("mask"), py::arg("lse2"), py::arg("scores"),
         py::arg("scale"), py::arg("q_offset"), py::arg("pages") = py::none());
   m.def("silu_mul", &silu_mul, "SwiGLU activation of [gate; up]");
-  m.def("glu", &glu_act, "act(gate) * up of [gate; up]: act 0 = SiLU, 1 = GELU (tanh approximation)");
+  m.def("glu", &glu_act, "act(gate) * up of [gate; up]: act 0 = SiLU, 1 = GELU (tanh approximation), 2 = clamped "
+        "SwiGLU with the given limit", py::arg("gu"), py::arg("act"), py::arg("limit") = 7.0);
   m.def("linear_parts", &linear_parts, "x @ w.T as bf16 or fp32 split-K partials for a fusing consumer");
   m.def("moe_route", &moe_route, "top-k expert routing with deterministic expert-order positions");
   m.def("moe_gather", &moe_gather, "permute token rows into expert order");

@@ -2,7 +2,7 @@
 //   * rmsnorm_kernel      fused residual add + RMSNorm (one CTA per token row, 16-byte vector loads)
 //   * rope_store_kernel   optional per-head RMSNorm (QK-norm families) + rotary embedding of q and k, and the
 //                         KV-cache write of k and v (one warp per token x head)
-//   * glu_kernel          SwiGLU / GeGLU activation of a fused [gate; up] projection
+//   * glu_kernel          SwiGLU / GeGLU / clamped SwiGLU activation of a fused [gate; up] projection
 //   * argmax_kernel       first index of the row maximum (one CTA per row)
 //   * greedy_accept_kernel longest accepted path of a verified draft tree (one warp per row)
 //   * kv_compact_kernel   moves the accepted path's K/V to consecutive slots in all layers at once
@@ -289,21 +289,34 @@ int launch_rope_store(const void* qkv, const int* positions, const float* cos_t,
 }
 
 // ---------------------------------------------------------------------------------------------------------------
-// act(gate) * up: SiLU (SwiGLU) or the tanh approximation of GELU (GeGLU, Gemma's gelu_pytorch_tanh)
+// act(gate) * up: SiLU (SwiGLU), the tanh approximation of GELU (GeGLU, Gemma's gelu_pytorch_tanh), or gpt-oss's
+// clamped SwiGLU: g = min(gate, limit), (clamp(up, -limit, limit) + 1) * g * sigmoid(1.702 g)
 // ---------------------------------------------------------------------------------------------------------------
 template <int kAct>
-__device__ __forceinline__ float glu_act(float x) {
+__device__ __forceinline__ float glu_act(float x, float limit) {
   if constexpr (kAct == 0) {
     return x / (1.f + expf(-x));
-  } else {  // 0.5 x (1 + tanh(sqrt(2 / pi) (x + 0.044715 x^3)))
+  } else if constexpr (kAct == 1) {  // 0.5 x (1 + tanh(sqrt(2 / pi) (x + 0.044715 x^3)))
     const float inner = 0.7978845608028654f * fmaf(0.044715f * x, x * x, x);
     return 0.5f * x * (1.f + tanhf(inner));
+  } else {
+    const float g = fminf(x, limit);
+    return g / (1.f + expf(-1.702f * g));
+  }
+}
+
+template <int kAct>
+__device__ __forceinline__ float glu_up(float u, float limit) {
+  if constexpr (kAct == 2) {
+    return fminf(fmaxf(u, -limit), limit) + 1.f;
+  } else {
+    return u;
   }
 }
 
 template <int kAct>
 __global__ void __launch_bounds__(256) glu_kernel(const bf16* __restrict__ gu, bf16* __restrict__ out, int rows,
-                                                  int F, Parts parts) {
+                                                  int F, Parts parts, float limit) {
   pdl_trigger();
   pdl_wait();
   const long total = static_cast<long>(rows) * (F / 8);
@@ -318,22 +331,22 @@ __global__ void __launch_bounds__(256) glu_kernel(const bf16* __restrict__ gu, b
     bf16* op = reinterpret_cast<bf16*>(&o);
 #pragma unroll
     for (int j = 0; j < 8; ++j) {
-      const float s = bf16r(glu_act<kAct>(__bfloat162float(gp[j])));
-      op[j] = __float2bfloat16(s * __bfloat162float(up[j]));
+      const float s = bf16r(glu_act<kAct>(__bfloat162float(gp[j]), limit));
+      op[j] = __float2bfloat16(s * glu_up<kAct>(__bfloat162float(up[j]), limit));
     }
     reinterpret_cast<uint4*>(out + r * F)[c] = o;
   }
 }
 
 int launch_glu(const void* gu, void* out, int rows, int F, cudaStream_t stream, const float* gu_parts, int splits,
-               int act) {
-  if (F % 8 != 0 || act < 0 || act > 1) return -1;
+               int act, float limit) {
+  if (F % 8 != 0 || act < 0 || act > 2) return -1;
   const Parts parts{gu_parts, splits, static_cast<long>(rows) * 2 * F};
   const long total = static_cast<long>(rows) * (F / 8);
   int blocks = static_cast<int>(std::min<long>((total + 255) / 256, 148L * 16));
   if (blocks < 1) blocks = 1;
-  launch_pdl(act == 0 ? glu_kernel<0> : glu_kernel<1>, dim3(blocks), dim3(256), 0, stream,
-             static_cast<const bf16*>(gu), static_cast<bf16*>(out), rows, F, parts);
+  launch_pdl(act == 0 ? glu_kernel<0> : act == 1 ? glu_kernel<1> : glu_kernel<2>, dim3(blocks), dim3(256), 0, stream,
+             static_cast<const bf16*>(gu), static_cast<bf16*>(out), rows, F, parts, limit);
   return 0;
 }
 

@@ -91,9 +91,11 @@ int launch_rope_store(const void* qkv, const int* positions, const float* cos_t,
                       cudaStream_t stream, const float* k_scale = nullptr, const float* v_scale = nullptr,
                       const float* qkv_parts = nullptr, int splits = 0, const KVPages& pages = KVPages(),
                       int table_rows = 1 << 30, unsigned* status = nullptr);
-// act(gate) * up of a fused [gate; up] projection: act 0 = SiLU, 1 = GELU (tanh approximation)
+// act(gate) * up of a fused [gate; up] projection: act 0 = SiLU, 1 = GELU (tanh approximation), 2 = clamped SwiGLU
+// ((clamp(up, -limit, limit) + 1) * g * sigmoid(1.702 g), g = min(gate, limit))
 int launch_glu(const void* gu, void* out, int rows, int F, cudaStream_t stream, const float* gu_parts, int splits,
-               int act);
+               int act,
+               float limit = 7.f);
 int launch_silu_mul(const void* gu, void* out, int rows, int F, cudaStream_t stream, const float* gu_parts = nullptr,
                     int splits = 0);
 int argmax_slices(int rows, int V);

@@ -15,8 +15,8 @@ import torch
 
 from ..errors import UnsupportedModelError
 
-__all__ = ["ModelConfig", "SUPPORTED_MODEL_TYPES", "llama31_8b", "llama31_70b", "mixtral_8x7b", "rope_inv_freq",
-           "tiny_llama"]
+__all__ = ["ModelConfig", "SUPPORTED_MODEL_TYPES", "gpt_oss_20b", "llama31_8b", "llama31_70b", "mixtral_8x7b",
+           "rope_attention_factor", "rope_inv_freq", "tiny_llama"]
 
 #: ``model_type`` values whose decoder layer is the Llama block (attention + gated MLP with RMSNorms), with the
 #: differences expressed as fields: q/k/v bias (qwen2), per-head q/k RMSNorm (qwen3, qwen3_moe), sparse MoE MLP
@@ -27,10 +27,11 @@ __all__ = ["ModelConfig", "SUPPORTED_MODEL_TYPES", "llama31_8b", "llama31_70b", 
 #: before and after each branch with tanh soft-capped attention scores and logits (gemma2) or per-head q/k norms and
 #: separate rotary tables for the sliding-window layers (gemma3_text), per-layer sliding windows (mistral, ministral,
 #: gemma2, gemma3_text, olmo3, qwen2 with use_sliding_window), sparse MoE with q/k norms (olmoe) and a gated shared
-#: expert (qwen2_moe).
+#: expert (qwen2_moe), and biased projections everywhere with attention sink logits, YaRN rotary scaling and
+#: clamped-SwiGLU experts (gpt_oss).
 SUPPORTED_MODEL_TYPES = ("llama", "mistral", "qwen2", "qwen3", "mixtral", "granite", "phi3", "smollm3", "olmo2",
                          "qwen3_moe", "gemma", "gemma2", "gemma3_text", "ministral", "olmo3", "olmoe", "qwen2_moe",
-                         "economize_b200")
+                         "gpt_oss", "economize_b200")
 
 #: the layer kinds of ``ModelConfig.layer_types``
 FULL, SLIDING = "full_attention", "sliding_attention"
@@ -69,8 +70,10 @@ class ModelConfig:
     qk_norm_full: bool = False
     #: layers whose attention runs without rotary embedding (SmolLM3's NoPE layers)
     nope_layers: tuple[int, ...] = ()
-    #: gated MLP activation: "silu" (SwiGLU) or "gelu_tanh" (GeGLU, Gemma)
+    #: gated MLP activation: "silu" (SwiGLU), "gelu_tanh" (GeGLU, Gemma) or "clamped_swiglu" (gpt-oss:
+    #: (clamp(up, +-swiglu_limit) + 1) * g * sigmoid(1.702 g), g = min(gate, swiglu_limit))
     hidden_act: str = "silu"
+    swiglu_limit: float = 7.0
     #: Gemma's RMSNorms scale by (1 + w): checkpoints store w, this model stores 1 + w
     norm_unit_offset: bool = False
     #: the embedding multiplier is rounded to the model dtype before it multiplies (Gemma's normalizer)
@@ -88,6 +91,11 @@ class ModelConfig:
     local_rope: dict[str, Any] | None = None
     #: width of a shared expert added to every sparse MoE MLP, gated by sigmoid(x . w) (Qwen2-MoE; 0: none)
     shared_expert_size: int = 0
+    #: gpt-oss: a bias on the attention output projection, one learned sink logit per query head that joins every
+    #: softmax denominator, and biases on the router and on both expert projections
+    o_bias: bool = False
+    attn_sinks: bool = False
+    moe_bias: bool = False
     extra: dict[str, Any] = field(default_factory=dict)
 
     def __post_init__(self) -> None:
@@ -97,7 +105,7 @@ class ModelConfig:
         self.layer_types = tuple(str(t) for t in self.layer_types)
         if self.num_heads % self.num_kv_heads:
             raise UnsupportedModelError(f"{self.num_heads} heads do not split into {self.num_kv_heads} KV groups")
-        if self.hidden_act not in ("silu", "gelu_tanh"):
+        if self.hidden_act not in ("silu", "gelu_tanh", "clamped_swiglu"):
             raise UnsupportedModelError(f"gated activation {self.hidden_act!r} is not supported")
         if self.layer_types and len(self.layer_types) != self.num_layers:
             raise UnsupportedModelError(f"{len(self.layer_types)} layer types for {self.num_layers} layers")
@@ -130,6 +138,9 @@ class ModelConfig:
         attn = h * (self.q_size + 2 * self.kv_size) + self.q_size * h
         mlp = 3 * h * f * (self.num_experts if self.is_moe else 1) + (h * self.num_experts if self.is_moe else 0)
         mlp += 3 * h * self.shared_expert_size + (h if self.shared_expert_size else 0)
+        if self.moe_bias:
+            mlp += self.num_experts * (2 * f + h + 1)
+        attn += (h if self.o_bias else 0) + (self.num_heads if self.attn_sinks else 0)
         embed = self.vocab_size * h * (1 if self.tie_word_embeddings else 2)
         return layers * (attn + mlp + 2 * h) + embed + h
 
@@ -191,6 +202,9 @@ class ModelConfig:
                 qpas = get("query_pre_attn_scalar")
                 extra.update(sandwich_norm=True, attention_multiplier=float(qpas) ** -0.5 if qpas else None,
                              attn_softcap=get("attn_logit_softcapping"), final_softcap=get("final_logit_softcapping"))
+        elif model_type == "gpt_oss":
+            extra.update(hidden_act="clamped_swiglu", swiglu_limit=float(get("swiglu_limit", 7.0) or 7.0),
+                         o_bias=True, attn_sinks=True, moe_bias=True)
         elif (get("hidden_act") or "silu") != "silu":
             raise UnsupportedModelError(f"{model_type}: activation {get('hidden_act')!r} is not supported")
         experts = int(get("num_local_experts", 0) or get("num_experts", 0) or 0)
@@ -271,6 +285,12 @@ class ModelConfig:
             return transformers.Gemma3TextConfig(rope_parameters={FULL: full, SLIDING: local},
                                                  attn_logit_softcapping=self.attn_softcap,
                                                  final_logit_softcapping=self.final_softcap, **gem)
+        if kind == "gpt_oss":
+            rope = {"rope_type": "default", "rope_theta": self.rope_theta, **(self.rope_scaling or {})}
+            gpt = {k: v for k, v in common.items() if k not in ("rope_theta", "rope_scaling", "attention_bias")}
+            return transformers.GptOssConfig(num_local_experts=self.num_experts,
+                                             num_experts_per_tok=self.experts_per_token, rope_parameters=rope,
+                                             attention_bias=self.attention_bias, **kinds, **gpt)
         if kind == "ministral":
             return transformers.MinistralConfig(**kinds, **{k: v for k, v in common.items() if k != "attention_bias"})
         if kind == "mistral":
@@ -342,9 +362,73 @@ def rope_inv_freq(config: ModelConfig, local: bool = False) -> torch.Tensor:
         inv = torch.where(medium, blended, scaled)
     elif kind == "linear":
         inv = inv / float(scaling["factor"])
+    elif kind == "yarn":
+        inv = _yarn_inv_freq(inv, dim, theta, scaling, config.max_position_embeddings)
     elif kind not in (None, "default"):
         raise UnsupportedModelError(f"rope_scaling type {kind!r} is not supported")
     return inv
+
+
+def _yarn_inv_freq(inv: torch.Tensor, dim: int, theta: float, scaling: dict[str, Any],
+                   max_positions: int) -> torch.Tensor:
+    """YaRN's frequency blend (Peng et al., 2023, "YaRN: Efficient Context Window Extension of Large Language
+    Models", section 3.2; the form of transformers ``modeling_rope_utils.py``, ``_compute_yarn_parameters``): a
+    frequency that turns fewer than ``beta_slow`` times over the original context is interpolated (divided by
+    ``factor``), one that turns more than ``beta_fast`` times is kept, and a linear ramp over the dimension index
+    blends the two in between. The dimension that turns ``r`` times is ``dim * ln(L / (2 pi r)) / (2 ln theta)``."""
+    factor = float(scaling.get("factor") or max_positions / float(scaling["original_max_position_embeddings"]))
+    original = float(scaling["original_max_position_embeddings"])
+    fast, slow = float(scaling.get("beta_fast") or 32), float(scaling.get("beta_slow") or 1)
+
+    def turning_dim(turns: float) -> float:
+        return dim * math.log(original / (turns * 2 * math.pi)) / (2 * math.log(theta))
+
+    low, high = turning_dim(fast), turning_dim(slow)
+    if scaling.get("truncate", True):
+        low, high = math.floor(low), math.ceil(high)
+    low, high = max(low, 0), min(high, dim - 1)
+    if low == high:
+        high += 0.001
+    ramp = ((torch.arange(dim // 2, dtype=torch.float32) - low) / (high - low)).clamp(0, 1)
+    keep = 1 - ramp  # 1: extrapolate (the original frequency), 0: interpolate
+    return (inv / factor) * (1 - keep) + inv * keep
+
+
+def rope_attention_factor(config: ModelConfig, local: bool = False) -> float:
+    """The factor YaRN applies to cos and sin (``attention_factor``, else ``0.1 ln(factor) + 1``, or its
+    ``mscale`` / ``mscale_all_dim`` ratio); 1 for every other rotary kind."""
+    scaling = config.rope_scaling or {}
+    if local and config.local_rope is not None:
+        scaling = config.local_rope
+    if scaling.get("rope_type", scaling.get("type")) != "yarn":
+        return 1.0
+    if scaling.get("attention_factor") is not None:
+        return float(scaling["attention_factor"])
+    factor = float(scaling.get("factor") or config.max_position_embeddings /
+                   float(scaling["original_max_position_embeddings"]))
+
+    def mscale(scale: float, m: float = 1.0) -> float:
+        return 1.0 if scale <= 1 else 0.1 * m * math.log(scale) + 1.0
+
+    m, m_all = scaling.get("mscale"), scaling.get("mscale_all_dim")
+    if m and m_all:
+        return mscale(factor, float(m)) / mscale(factor, float(m_all))
+    return mscale(factor)
+
+
+def gpt_oss_20b(**overrides: Any) -> ModelConfig:
+    """gpt-oss-20b architecture (24 layers, hidden 2880, 64/8 heads of 64, 32 experts of width 2880, top-4; 128-token
+    windows on the even layers; YaRN x32 over 4096 positions; biases everywhere and sink logits)."""
+    layers = int(overrides.pop("num_layers", 24))
+    cfg = dict(vocab_size=201088, hidden_size=2880, intermediate_size=2880, num_layers=layers, num_heads=64,
+               num_kv_heads=8, head_dim=64, rms_norm_eps=1e-5, rope_theta=150000.0,
+               rope_scaling={"rope_type": "yarn", "factor": 32.0, "beta_fast": 32.0, "beta_slow": 1.0,
+                             "truncate": False, "original_max_position_embeddings": 4096},
+               max_position_embeddings=131072, attention_bias=True, num_experts=32, experts_per_token=4,
+               model_type="gpt_oss", hidden_act="clamped_swiglu", o_bias=True, attn_sinks=True, moe_bias=True,
+               layer_types=tuple(SLIDING if i % 2 == 0 else FULL for i in range(layers)), sliding_window=128)
+    cfg.update(overrides)
+    return ModelConfig(**cfg)
 
 
 def llama31_8b(**overrides: Any) -> ModelConfig:

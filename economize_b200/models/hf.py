@@ -5,7 +5,9 @@ same norm kernel; sandwich blocks (Gemma-2/3) map four norms per block.
 
 Names follow ``transformers`` 5 (``model.layers.{i}.self_attn.q_proj.weight`` ..., Mixtral experts as fused
 ``mlp.experts.gate_up_proj [E, 2F, H]`` / ``down_proj [E, H, F]``; the older per-expert ``block_sparse_moe.experts.
-{e}.w1/w2/w3`` layout is read too).
+{e}.w1/w2/w3`` layout is read too). gpt-oss stores its experts input-major with gate and up interleaved
+(``gate_up_proj [E, H, 2F]``, gate in the even columns; ``down_proj [E, F, H]``) and its router as
+``mlp.router.{weight, bias}``; they are transposed and de-interleaved into the fused ``[gate; up]`` rows here.
 """
 
 from __future__ import annotations
@@ -50,6 +52,8 @@ def load_hf_state(model, state: dict[str, torch.Tensor]) -> None:
         if layer.bqkv is not None:
             layer.bqkv.copy_(torch.cat([_take(state, a + f"{n}_proj.bias") for n in "qkv"], 0))
         layer.wo.copy_(_take(state, a + "o_proj.weight"))
+        if layer.bo is not None:
+            layer.bo.copy_(_take(state, a + "o_proj.bias"))
         if layer.q_norm is not None:
             layer.q_norm.copy_(_norm_in(c, _take(state, a + "q_norm.weight")))
             layer.k_norm.copy_(_norm_in(c, _take(state, a + "k_norm.weight")))
@@ -57,7 +61,17 @@ def load_hf_state(model, state: dict[str, torch.Tensor]) -> None:
             getattr(layer, ours).copy_(_norm_in(c, _take(state, p + theirs + ".weight")))
         if layer.sinks is not None and a + "sinks" in state:
             layer.sinks.copy_(state[a + "sinks"])
-        if c.is_moe:
+        if c.is_moe and c.model_type == "gpt_oss":
+            x = p + "mlp.experts."
+            layer.router.copy_(_take(state, p + "mlp.router.weight"))
+            layer.router_bias.copy_(_take(state, p + "mlp.router.bias"))
+            gu = _take(state, x + "gate_up_proj").transpose(1, 2)  # [E, 2F, H], gate rows even
+            layer.w_gate_up.copy_(torch.cat([gu[:, 0::2], gu[:, 1::2]], 1))
+            b = _take(state, x + "gate_up_proj_bias")
+            layer.b_gate_up.copy_(torch.cat([b[:, 0::2], b[:, 1::2]], 1))
+            layer.w_down.copy_(_take(state, x + "down_proj").transpose(1, 2))
+            layer.b_down.copy_(_take(state, x + "down_proj_bias"))
+        elif c.is_moe:
             if p + "mlp.experts.gate_up_proj" in state:
                 layer.router.copy_(_take(state, p + "mlp.gate.weight"))
                 layer.w_gate_up.copy_(state[p + "mlp.experts.gate_up_proj"])
@@ -124,6 +138,8 @@ def export_hf_state(model, copy: bool = True) -> dict[str, torch.Tensor]:
             for n, w in zip("qkv", layer.bqkv.detach().split([c.q_size, c.kv_size, c.kv_size], 0)):
                 out[p + f"self_attn.{n}_proj.bias"] = w
         out[p + "self_attn.o_proj.weight"] = full(layer.wo)
+        if layer.bo is not None:
+            out[p + "self_attn.o_proj.bias"] = layer.bo.detach()
         if layer.q_norm is not None:
             out[p + "self_attn.q_norm.weight"] = _norm_out(c, layer.q_norm)
             out[p + "self_attn.k_norm.weight"] = _norm_out(c, layer.k_norm)
@@ -131,7 +147,17 @@ def export_hf_state(model, copy: bool = True) -> dict[str, torch.Tensor]:
             out[p + theirs + ".weight"] = _norm_out(c, getattr(layer, ours))
         if layer.sinks is not None:
             out[p + "self_attn.sinks"] = layer.sinks.detach()
-        if c.is_moe:
+        if c.is_moe and c.model_type == "gpt_oss":
+            x = p + "mlp.experts."
+            out[p + "mlp.router.weight"] = layer.router.detach()
+            out[p + "mlp.router.bias"] = layer.router_bias.detach()
+            g, u = full(layer.w_gate_up).chunk(2, 1)  # [E, F, H] each
+            out[x + "gate_up_proj"] = torch.stack([g, u], 2).reshape(g.shape[0], -1, g.shape[2]).transpose(1, 2)
+            bg, bu = layer.b_gate_up.detach().chunk(2, 1)
+            out[x + "gate_up_proj_bias"] = torch.stack([bg, bu], 2).reshape(bg.shape[0], -1)
+            out[x + "down_proj"] = full(layer.w_down).transpose(1, 2)
+            out[x + "down_proj_bias"] = layer.b_down.detach()
+        elif c.is_moe:
             out[p + "mlp.gate.weight"] = layer.router.detach()
             out[p + "mlp.experts.gate_up_proj"] = full(layer.w_gate_up)
             out[p + "mlp.experts.down_proj"] = full(layer.w_down)

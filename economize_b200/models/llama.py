@@ -26,7 +26,7 @@ from torch import nn
 from .. import ops
 from ..errors import ConfigError
 from ..runtime.cache import KVCache, PagedKVCache, SplitKVCache, StepBatch
-from .config import ModelConfig, rope_inv_freq
+from .config import ModelConfig, rope_attention_factor, rope_inv_freq
 
 __all__ = ["CausalLM", "DecoderLayer", "init_weights"]
 
@@ -43,6 +43,7 @@ class DecoderLayer(nn.Module):
         self.bqkv = nn.Parameter(torch.zeros(config.q_size + 2 * config.kv_size, **kw)) if config.attention_bias \
             else None
         self.wo = nn.Parameter(torch.empty(h, config.q_size, **kw))
+        self.bo = nn.Parameter(torch.zeros(h, **kw)) if config.o_bias else None
         # q/k RMSNorm weights: one head's width (per-head norm) or all heads' (a norm over the whole projection)
         qn, kn = (config.q_size, config.kv_size) if config.qk_norm_full else (config.head_dim, config.head_dim)
         self.q_norm = nn.Parameter(torch.ones(qn, **kw)) if config.qk_norm else None
@@ -56,13 +57,20 @@ class DecoderLayer(nn.Module):
         self.w_shared_gate_up = nn.Parameter(torch.empty(2 * se, h, **kw)) if se else None
         self.w_shared_down = nn.Parameter(torch.empty(h, se, **kw)) if se else None
         self.shared_gate = nn.Parameter(torch.empty(1, h, **kw)) if se else None
-        #: attention sink logits of this layer's query heads (fp32 [H]; gpt-oss-style models), or None
-        self.sinks = None
+        #: attention sink logits of this layer's query heads (fp32 [H]; gpt-oss), or None
+        self.sinks = nn.Parameter(torch.zeros(config.num_heads, dtype=torch.float32, device=device)) \
+            if config.attn_sinks else None
+        # gpt-oss: biases of the router [E] and of every expert's projections ([E, 2F] as [gate; up], [E, H])
+        self.router_bias = self.b_gate_up = self.b_down = None
         if config.is_moe:
             e = config.num_experts
             self.router = nn.Parameter(torch.empty(e, h, **kw))
             self.w_gate_up = nn.Parameter(torch.empty(e, 2 * f, h, **kw))
             self.w_down = nn.Parameter(torch.empty(e, h, f, **kw))
+            if config.moe_bias:
+                self.router_bias = nn.Parameter(torch.zeros(e, **kw))
+                self.b_gate_up = nn.Parameter(torch.zeros(e, 2 * f, **kw))
+                self.b_down = nn.Parameter(torch.zeros(e, h, **kw))
         else:
             self.router = None
             self.w_gate_up = nn.Parameter(torch.empty(2 * f, h, **kw))
@@ -141,6 +149,9 @@ class CausalLM(nn.Module):
             pos = torch.arange(need, device=self.device, dtype=torch.float32)
             angles = pos[:, None] * inv[None, :]
             cached = (angles.cos().contiguous(), angles.sin().contiguous())
+            factor = rope_attention_factor(self.config, local=local)
+            if factor != 1.0:  # YaRN scales cos and sin (and so both q and k)
+                cached = (cached[0] * factor, cached[1] * factor)
             if local:
                 self._rope_local = cached
             else:
@@ -427,7 +438,11 @@ class CausalLM(nn.Module):
         o = self._attend(layer, index, qkv, batch, cache, cos, sin)
         if self.observer is not None:
             self.observer(index, "wo", o)
-        return self._row_linear(o, layer.wo)
+        if layer.bo is None:
+            return self._row_linear(o, layer.wo)
+        # the output bias joins once: on rank 0's partial sum under tensor parallelism
+        first = self.tp is None or self.tp.size == 1 or self.tp.rank == 0
+        return ops.linear(o, layer.wo, layer.bo if first else None)
 
     def _attend(self, layer: DecoderLayer, index: int, qkv, batch: StepBatch, cache: KVCache, cos: torch.Tensor,
                 sin: torch.Tensor) -> torch.Tensor:
@@ -463,7 +478,8 @@ class CausalLM(nn.Module):
         tail = self.exact_tail if (not batch.prompt and q.shape[1] <= 64 and not sparse_pass) else 0
         o = ops.attention(q, k_cache, v_cache, batch.kv_len, batch.n_new, batch.mask, scale=c.attention_multiplier,
                           q_offset=batch.q_offset, k_scale=k_scale, v_scale=v_scale, keep=keep, tail=tail,
-                          softcap=c.attn_softcap, sinks=layer.sinks, window=c.window_of(index), pages=pages,
+                          softcap=c.attn_softcap, sinks=None if layer.sinks is None else layer.sinks.float(),
+                          window=c.window_of(index), pages=pages,
                           **kivi)
         if self.kv_evictor is not None and batch.is_prefill:
             self.kv_evictor.observe_prefill(index, q, k_cache, v_cache, batch)
@@ -490,8 +506,11 @@ class CausalLM(nn.Module):
         if layer.router is not None:
             from ..parallel.moe import moe_mlp
 
-            out = moe_mlp(x, layer.router, layer.w_gate_up, layer.w_down, self.config.experts_per_token,
-                          getattr(self, "ep", None), renormalize=self.config.norm_topk_prob)
+            c = self.config
+            biases = None if layer.router_bias is None else (layer.router_bias, layer.b_gate_up, layer.b_down)
+            out = moe_mlp(x, layer.router, layer.w_gate_up, layer.w_down, c.experts_per_token,
+                          getattr(self, "ep", None), renormalize=c.norm_topk_prob, act=c.hidden_act,
+                          limit=c.swiglu_limit, biases=biases)
             if layer.w_shared_gate_up is not None:  # Qwen2-MoE's gated shared expert
                 shared = ops.linear(ops.silu_mul(ops.linear(x, layer.w_shared_gate_up)), layer.w_shared_down)
                 gate = torch.sigmoid(ops.linear(x, self._gate_rows(layer))[..., :1])
@@ -504,7 +523,7 @@ class CausalLM(nn.Module):
             out = rule(self, layer, x, index)
             if out is not None:
                 return out
-        a = ops.glu(self._linear(x, layer.w_gate_up), self.config.hidden_act)
+        a = ops.glu(self._linear(x, layer.w_gate_up), self.config.hidden_act, self.config.swiglu_limit)
         if self.observer is not None:
             self.observer(index, "w_down", a)
         return self._row_linear(a, layer.w_down)

@@ -221,12 +221,18 @@ def gelu_tanh_mul(gate_up: torch.Tensor | Partials) -> torch.Tensor:
     return reference.gelu_tanh_mul(gate_up.sum() if isinstance(gate_up, Partials) else gate_up)
 
 
-def glu(gate_up: torch.Tensor | Partials, act: str = "silu") -> torch.Tensor:
-    """The gated MLP activation ``act(gate) * up`` (``"silu"``: SwiGLU, ``"gelu_tanh"``: GeGLU)."""
+def glu(gate_up: torch.Tensor | Partials, act: str = "silu", limit: float = 7.0) -> torch.Tensor:
+    """The gated MLP activation ``act(gate) * up`` (``"silu"``: SwiGLU, ``"gelu_tanh"``: GeGLU,
+    ``"clamped_swiglu"``: gpt-oss's ``(clamp(up, +-limit) + 1) * g * sigmoid(1.702 g)`` with ``g = min(gate,
+    limit)``)."""
     if act == "silu":
         return silu_mul(gate_up)
     if act == "gelu_tanh":
         return gelu_tanh_mul(gate_up)
+    if act == "clamped_swiglu":
+        if gate_up.is_cuda:
+            return require().glu(_raw(gate_up), 2, limit)
+        return reference.clamped_swiglu(gate_up.sum() if isinstance(gate_up, Partials) else gate_up, limit)
     raise ValueError(f"unsupported gated activation {act!r}")
 
 

@@ -202,6 +202,16 @@ def gelu_tanh_mul(gate_up: torch.Tensor) -> torch.Tensor:
     return F.gelu(gate, approximate="tanh") * up
 
 
+def clamped_swiglu(gate_up: torch.Tensor, limit: float = 7.0) -> torch.Tensor:
+    """gpt-oss's gated activation of ``[gate; up]``: ``g = min(gate, limit)``, ``(clamp(up, -limit, limit) + 1) *
+    g * sigmoid(1.702 g)`` (transformers ``models/gpt_oss/modeling_gpt_oss.py``, ``GptOssExperts._apply_gate``, with
+    gate and up as halves instead of interleaved columns)."""
+    gate, up = gate_up.chunk(2, -1)
+    gate = gate.clamp(max=limit)
+    up = up.clamp(-limit, limit)
+    return (up + 1) * (gate * torch.sigmoid(gate * 1.702))
+
+
 def linear(x: torch.Tensor, weight: torch.Tensor, bias: torch.Tensor | None = None) -> torch.Tensor:
     return F.linear(x, weight, bias)
 

@@ -39,12 +39,16 @@ def route(logits: torch.Tensor, k: int) -> tuple[torch.Tensor, torch.Tensor]:
 
 
 def moe_reference(x: torch.Tensor, router: torch.Tensor, w_gate_up: torch.Tensor, w_down: torch.Tensor,
-                  k: int, renormalize: bool = True, logits: torch.Tensor | None = None) -> torch.Tensor:
+                  k: int, renormalize: bool = True, logits: torch.Tensor | None = None, act: str = "silu",
+                  limit: float = 7.0, biases: tuple[torch.Tensor, torch.Tensor, torch.Tensor] | None = None
+                  ) -> torch.Tensor:
     """The MoE MLP in plain PyTorch (fp32 accumulation of the weighted expert outputs); ``logits`` overrides the
-    router output (to route exactly like another implementation)."""
+    router output (to route exactly like another implementation). ``act``: the gated activation of
+    :func:`economize_b200.ops.glu`; ``biases``: (router [E], gate/up [E, 2F], down [E, H]) of gpt-oss experts."""
     shape = x.shape
     x2 = x.reshape(-1, shape[-1])
-    scores = F.linear(x2, router) if logits is None else logits
+    b_router, b_gate_up, b_down = biases if biases is not None else (None, None, None)
+    scores = F.linear(x2, router, b_router) if logits is None else logits
     ids, w = route(scores, k)
     if not renormalize:
         w = w * torch.softmax(scores.float(), -1).gather(-1, ids).sum(-1, keepdim=True).to(w.dtype)
@@ -53,36 +57,55 @@ def moe_reference(x: torch.Tensor, router: torch.Tensor, w_gate_up: torch.Tensor
         rows, slot = (ids == e).nonzero(as_tuple=True)
         if rows.numel() == 0:
             continue
-        g, u = F.linear(x2[rows], w_gate_up[e]).chunk(2, -1)
-        y = F.linear(F.silu(g) * u, w_down[e])
+        gu = F.linear(x2[rows], w_gate_up[e], None if b_gate_up is None else b_gate_up[e])
+        y = F.linear(ops.glu(gu, act, limit), w_down[e], None if b_down is None else b_down[e])
         out.index_add_(0, rows, y.float() * w[rows, slot][:, None])
     return out.to(x.dtype).reshape(shape)
 
 
+def _expert_rows(offsets: torch.Tensor, rows: int) -> torch.Tensor:
+    """The expert of every expert-ordered row (``offsets [E + 1]``), found on the device without a host sync."""
+    return torch.searchsorted(offsets[1:].contiguous(), torch.arange(rows, device=offsets.device, dtype=torch.int32),
+                              right=True)
+
+
 def moe_mlp(x: torch.Tensor, router: torch.Tensor, w_gate_up: torch.Tensor, w_down: torch.Tensor,
-            k: int, ep: ExpertParallel | None = None, renormalize: bool = True) -> torch.Tensor:
+            k: int, ep: ExpertParallel | None = None, renormalize: bool = True, act: str = "silu",
+            limit: float = 7.0, biases: tuple[torch.Tensor, torch.Tensor, torch.Tensor] | None = None
+            ) -> torch.Tensor:
     """Top-``k`` MoE MLP of ``x [..., H]`` with experts ``w_gate_up [E, 2F, H]``, ``w_down [E, H, F]``. The
-    chosen experts' softmax probabilities are renormalised to sum to one (Mixtral), or kept as they are
-    (``renormalize=False``, Qwen3-MoE's ``norm_topk_prob=False``)."""
+    chosen experts' softmax probabilities are renormalised to sum to one (Mixtral; for gpt-oss this is its softmax
+    over the top-k logits), or kept as they are (``renormalize=False``, Qwen3-MoE's ``norm_topk_prob=False``).
+    ``act`` is the experts' gated activation and ``biases`` the gpt-oss router and expert biases (router [E],
+    gate/up [E, 2F], down [E, H]): on the GPU each grouped GEMM's rows get their expert's bias before the
+    activation and before the weighted combine."""
     if ep is not None and ep.size > 1:
         if not renormalize:
             raise ConfigError("expert parallelism renormalises the top-k router weights")
+        if act != "silu" or biases is not None:
+            raise ConfigError("expert parallelism runs SwiGLU experts without biases")
         return ep.forward(x, router, w_gate_up, w_down, k)
     if not x.is_cuda:
-        return moe_reference(x, router, w_gate_up, w_down, k, renormalize)
+        return moe_reference(x, router, w_gate_up, w_down, k, renormalize, act=act, limit=limit, biases=biases)
     from ..ops._ext import require
 
     C = require()
     shape = x.shape
     x2 = x.reshape(-1, shape[-1]).contiguous()
-    logits = ops.linear(x2, router)
+    logits = ops.linear(x2, router, None if biases is None else biases[0])
     ids, weights, pos, offsets = C.moe_route(logits, k)
     if not renormalize:  # back from the renormalised weights to the softmax probabilities of the chosen experts
         chosen = torch.softmax(logits.float(), -1).gather(-1, ids.long()).sum(-1, keepdim=True)
         weights = weights * chosen
     xs = C.moe_gather(x2, pos)
-    a = ops.silu_mul(C.linear_grouped(xs, w_gate_up, offsets))
+    gu = C.linear_grouped(xs, w_gate_up, offsets)
+    if biases is not None:
+        expert = _expert_rows(offsets, gu.shape[0])
+        gu = gu + biases[1].index_select(0, expert)
+    a = ops.glu(gu, act, limit)
     y = C.linear_grouped(a, w_down, offsets)
+    if biases is not None:
+        y = y + biases[2].index_select(0, expert)
     return C.moe_combine(y, pos, weights).reshape(shape)
 
 

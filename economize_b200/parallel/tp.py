@@ -85,6 +85,8 @@ def shard_model(model, tp: TPGroup):
             layer.bqkv.data = torch.cat([bq[r * hq * d:(r + 1) * hq * d], bk[r * hkv * d:(r + 1) * hkv * d],
                                          bv[r * hkv * d:(r + 1) * hkv * d]], 0).contiguous()
         layer.wo.data = layer.wo.data[:, r * hq * d:(r + 1) * hq * d].contiguous()
+        if layer.sinks is not None:  # one sink logit per query head: this rank's heads
+            layer.sinks.data = layer.sinks.data[r * hq:(r + 1) * hq].contiguous()
         gate, up = layer.w_gate_up.data.chunk(2, 0)
         layer.w_gate_up.data = torch.cat([gate[r * f:(r + 1) * f], up[r * f:(r + 1) * f]], 0).contiguous()
         layer.w_down.data = layer.w_down.data[:, r * f:(r + 1) * f].contiguous()

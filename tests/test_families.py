@@ -37,6 +37,11 @@ FAMILIES = {
     "olmoe": dict(num_experts=4, num_experts_per_tok=2, norm_topk_prob=False),
     "qwen2_moe": dict(num_experts=4, num_experts_per_tok=2, moe_intermediate_size=48,
                       shared_expert_intermediate_size=40, norm_topk_prob=False),
+    # biased q/k/v/o, sink logits, sliding windows on alternate layers, YaRN, clamped-SwiGLU experts with biases
+    "gpt_oss": dict(head_dim=16, num_local_experts=4, num_experts_per_tok=2, sliding_window=6,
+                    rope_parameters={"rope_type": "yarn", "factor": 4.0, "beta_fast": 32.0, "beta_slow": 1.0,
+                                     "truncate": False, "original_max_position_embeddings": 64,
+                                     "rope_theta": 10000.0}),
 }
 
 
@@ -51,6 +56,8 @@ def _hf(name, seed=0):
                 p.normal_(0, 0.2)
             elif "norm" in n:
                 p.uniform_(0.5, 1.5)
+            elif name == "gpt_oss":  # biases and sink logits
+                p.normal_(0, 0.5)
     return model
 
 

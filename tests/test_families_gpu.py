@@ -34,6 +34,9 @@ FAMILIES = {
     "olmoe": dict(num_experts=8, num_experts_per_tok=2, norm_topk_prob=False, intermediate_size=256),
     "qwen2_moe": dict(num_experts=8, num_experts_per_tok=2, moe_intermediate_size=256,
                       shared_expert_intermediate_size=384, norm_topk_prob=False),
+    # biased projections, sink logits, sliding windows on alternate layers, YaRN, clamped-SwiGLU biased experts
+    "gpt_oss": dict(head_dim=64, num_local_experts=8, num_experts_per_tok=4, intermediate_size=256,
+                    sliding_window=80),
 }
 
 
@@ -42,6 +45,11 @@ def test_family_on_gpu(cuda, name):
     cfg = transformers.CONFIG_MAPPING[name](**{**BASE, **FAMILIES[name]})
     torch.manual_seed(0)
     hf = transformers.AutoModelForCausalLM.from_config(cfg, attn_implementation="eager").float().eval()
+    if name == "gpt_oss":  # non-zero biases and sink logits, so their kernels' paths count
+        with torch.no_grad():
+            for n, p in hf.named_parameters():
+                if p.dim() == 1 and "norm" not in n or n.endswith("_bias"):
+                    p.normal_(0, 0.1)
     cpu = CausalLM.from_hf(hf)
     gpu = CausalLM.from_hf(hf, dtype=torch.bfloat16, device=cuda)
     ids = torch.randint(1, 1024, (1, 160), generator=torch.Generator().manual_seed(1))  # longer than the windows
