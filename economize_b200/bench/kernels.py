@@ -153,10 +153,62 @@ def bench_attention(a) -> None:
         ops.attention(q, k, v, kv_len, n_new, mask)
         torch.cuda.synchronize()
         return
+    if a.trace:
+        _attention_timeline(q, k, v, kv_len, n_new, mask, a)
+        return
     ours = time_graph([lambda: ops.attention(q, k, v, kv_len, n_new, mask)] * 8, a.iters, a.warmup)
     nbytes = 2 * (2 * B * Hkv * (a.ctx + T) * D + 2 * B * T * H * D)
     flops = 4 * B * T * H * (a.ctx + T) * D
     _report("attention", {"B": B, "T": T, "H": H, "Hkv": Hkv, "ctx": a.ctx}, ours, nbytes, flops)
+
+
+def _steady_phases(st, med) -> dict:
+    """Phase times in SM cycles of the pipelined walk's third chunk (stamps 8-15: loop top, scores ready, loads
+    issued, row maxima shared, previous P . V done, P stored, P visible to the MMA issuer, P . V issued)."""
+    fine = st[st[:, 15] != 0]
+    if fine.shape[0] == 0:
+        return {}
+    names = ["wait_s", "issue", "max", "wait_pv", "p_store", "sync", "pv_issue"]
+    out = {f"c2_{n}_cyc": int(med(fine[:, 9 + j] - fine[:, 8 + j]) * 1e3) for j, n in enumerate(names)}
+    out["c2_total_cyc"] = int(med(fine[:, 15] - fine[:, 8]) * 1e3)
+    return out
+
+
+def _attention_timeline(q, k, v, kv_len, n_new, mask, a) -> None:
+    """Per-CTA phase times of the attention kernel from its global-timer stamps (start, TMEM + Q staged, first K/V
+    chunk landed, first S MMA done, first softmax done, first PV MMA done, chunk loop done, end): medians over the
+    CTAs, the number of CTAs resident at once, and the kernel's span from the first start to the last end."""
+    from .. import ops
+
+    C = ops.require()
+    B, T, H, D = q.shape
+    Hkv, S = k.shape[1], k.shape[2]
+    most = B * Hkv * -(-T * (H // Hkv) // 128) * (S // 128)
+    trace = torch.zeros(most * 16, dtype=torch.int64, device=q.device)
+    for _ in range(a.warmup):
+        ops.attention(q, k, v, kv_len, n_new, mask)
+    C.attention(q, k, v, kv_len, n_new, mask, D ** -0.5, 0, trace)
+    torch.cuda.synchronize()
+    st = trace.view(-1, 16).cpu()
+    st = st[st[:, 0] != 0].double()
+    if st.shape[0] == 0:
+        print(json.dumps({"op": "attention_timeline", "error": "no stamps"}))
+        return
+    span_us = float((st[:, 7].max() - st[:, 0].min()) / 1e3)
+    med = lambda x: round(float(x.median()) / 1e3, 3)  # noqa: E731
+    sms = torch.cuda.get_device_properties(q.device).multi_processor_count
+    _, splits, chunks = C.attention_plan(B, T, H, Hkv, S, sms)
+    starts = st[:, 0].sort().values
+    ends = st[:, 7].sort().values
+    resident = int(max(((starts <= t0) & (ends > t0)).sum() for t0 in starts[:: max(1, len(starts) // 64)]))
+    print(json.dumps({"op": "attention_timeline", "T": T, "ctx": a.ctx, "ctas": int(st.shape[0]),
+                      "resident_max": resident, "span_us": round(span_us, 2),
+                      "setup_us": med(st[:, 1] - st[:, 0]), "first_kv_us": med(st[:, 2] - st[:, 0]),
+                      "s_mma_us": med(st[:, 3] - st[:, 2]), "softmax_us": med(st[:, 4] - st[:, 3]),
+                      "pv_us": med(st[:, 5] - st[:, 4]), "loop_us": med(st[:, 6] - st[:, 2]),
+                      "epilogue_us": med(st[:, 7] - st[:, 6]), "cta_us": med(st[:, 7] - st[:, 0]),
+                      **_steady_phases(st, med),
+                      "splits": int(splits), "chunks_per_split": int(chunks)}))
 
 
 def bench_layer(a) -> None:
@@ -281,6 +333,7 @@ def main(argv: list[str] | None = None) -> None:
     p.add_argument("--iters", type=int, default=20)
     p.add_argument("--warmup", type=int, default=3)
     p.add_argument("--once", action="store_true", help="one untimed call (for profiler captures)")
+    p.add_argument("--trace", action="store_true", help="attention: per-CTA phase timeline from the kernel's stamps")
     a = p.parse_args(argv)
     {"gemm": bench_gemm, "gemm_sweep": bench_gemm_sweep, "gemm_wq": bench_gemm_wq, "attention": bench_attention, "layer": bench_layer,
      "teal": bench_teal, "glu": bench_glu, "topk": bench_topk}[a.op](a)

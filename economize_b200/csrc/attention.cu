@@ -36,12 +36,22 @@
 // partials share the P tile), so K of the next chunk streams while P . V runs and V while the next S runs; the
 // accumulator uses TMEM columns [128, 384) of a 512-column allocation.
 //
+// Pipelined walk (bf16 caches without KIVI codes at head dimension 64 / 128, the PIPE instantiation): the scores
+// are double-buffered in TMEM (columns [0, 128) and [128, 256)) and the output accumulates in TMEM (columns from
+// 256), so the tensor cores compute S of chunk i + 1 while the threads run chunk i's softmax, and P . V of chunk i
+// accumulates into O without a per-chunk read of the accumulator. The running maximum is rescaled lazily: a row keeps
+// its reference maximum until a chunk raises it by more than kLazyLog2 (P then stays below 2^kLazyLog2), and only
+// then are its O columns read, scaled and written back (the per-row decision keeps a row's arithmetic independent
+// of the other rows, which the exact-tail guarantee needs). K and V stream on their own barriers: K of chunk i + 2
+// loads as soon as S of chunk i has read its stage, V of chunk i + 1 as soon as P . V of chunk i - 1 has.
+//
 // fp8 caches (e4m3 codes with one static scale per KV head, K = s_k * K8, V = s_v * V8): TMA brings the raw
 // [128 keys, 128 B] code tiles into a double-buffered staging ring, all threads convert them to bf16 (exact: every
 // e4m3 value is a bf16 value) in the swizzled layout the UMMAs read, and the scales are applied outside the tensor
 // cores: s_k multiplies the softmax scale, s_v the output. This reads half the bytes of a bf16 cache (the
 // reference's fp8_kv decode path decodes the codes in registers, src/economize/attention/_decode_kernels.py:17).
 #include <algorithm>
+#include <cstdlib>
 
 #include <cuda_fp8.h>
 
@@ -63,6 +73,13 @@ __host__ __device__ constexpr int attn_smem_bytes(int D) {
   return D == 256 ? kRows * D * 2 + kTile + 2 * kKeys * D * 2 + 1024 + 64  // one K/V stage; partials in the P tile
                   : kRows * D * 2 + kTile + 4 * kKeys * D * 2 + 1024 + 64 + 4 * 128 * 4;
 }
+// The pipelined walk keeps Q and P in TMEM: the shared memory holds kPipeStages rings of K and V chunks, the
+// barriers (128 B) and the row partials.
+__host__ __device__ constexpr int pipe_stages(int D) { return D == 64 ? 6 : 3; }
+__host__ __device__ constexpr int attn_pipe_smem_bytes(int D) {
+  return 2 * pipe_stages(D) * kKeys * D * 2 + 1024 + 128 + 4 * 128 * 4;
+}
+static_assert(attn_pipe_smem_bytes(128) <= 232448 && attn_pipe_smem_bytes(64) <= 232448, "pipelined rings fit");
 static_assert(attn_smem_bytes(256) <= 232448, "the D = 256 layout must fit 227 KB");
 static_assert(attn_smem_bytes(128) == kSmem, "the D = 128 layout is the reference footprint");
 constexpr int kRawTile = kKeys * kDim;                        // one fp8 code tile (128 keys x 128 B)
@@ -241,7 +258,10 @@ __device__ __forceinline__ void merge_row(const float* __restrict__ ws_o, const 
 // [32 * (w / 4), 32 * (w / 4) + 32) of them (quarter q).
 constexpr int kThreads = 512;
 
-template <bool FP8, int D = 128>
+// a row's reference maximum moves when a chunk raises it by more than this (log2 units; P < 2^kLazyLog2)
+constexpr float kLazyLog2 = 8.f;
+
+template <bool FP8, int D = 128, bool PIPE = false>
 __global__ void __launch_bounds__(kThreads, 1)
     attn_tc_kernel(const bf16* __restrict__ q, const __grid_constant__ CUtensorMap tm_k,
                    const __grid_constant__ CUtensorMap tm_v, bf16* __restrict__ out, float* __restrict__ ws_o,
@@ -256,33 +276,39 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   static_assert(D == 64 || D == 128 || D == 256, "head dimensions 64, 128 and 256");
   static_assert(!FP8 || D == 128, "fp8 caches at head dimension 128");
+  static_assert(!PIPE || (!FP8 && D <= 128), "the pipelined walk reads bf16 caches at head dimension 64 / 128");
   constexpr bool kSingle = D == 256;       // one K/V stage (see the file comment)
   constexpr int kQTile = kRows * D * 2;    // Q [128 rows, D]
   constexpr int kKVTile = kKeys * D * 2;   // one K or V chunk [128 keys, D]
   constexpr int kDQ = D / 4;               // output columns per quarter of the CTA
   constexpr int kAtoms = D / 64;           // 64-column swizzled atoms per row
   constexpr int kStages = kSingle ? 1 : 2;
-  constexpr uint32_t kTmemCols = kSingle ? 512 : 256;
+  constexpr uint32_t kTmemCols = (kSingle || PIPE) ? 512 : 256;
+  constexpr int kRing = pipe_stages(D);  // PIPE: depth of the K and V rings
   uint8_t* q_tile = smem;
   uint8_t* p_tile = smem + kQTile;
-  // bf16: kStages stages of K and V tiles; fp8: one converted K and V tile, then two stages of raw codes
-  uint8_t* k_tiles = p_tile + kTile;
-  uint8_t* v_tiles = FP8 ? k_tiles + kTile : k_tiles + kStages * kKVTile;
+  // bf16: kStages stages of K and V tiles; fp8: one converted K and V tile, then two stages of raw codes;
+  // PIPE: kRing stages of K, then kRing of V, from the start (Q and P live in TMEM)
+  uint8_t* k_tiles = PIPE ? smem : p_tile + kTile;
+  uint8_t* v_tiles = PIPE ? smem + kRing * kKVTile : FP8 ? k_tiles + kTile : k_tiles + kStages * kKVTile;
   uint8_t* raw = smem + 4 * kTile;  // fp8 stage s: raw K at s * 2 * kRawTile, raw V after it
-  // kv_full[s]: stage s of K and V (kSingle: [0] = K, [1] = V)
-  uint64_t* kv_full = reinterpret_cast<uint64_t*>(p_tile + kTile + 2 * kStages * kKVTile);
-  uint64_t* bar_s = kv_full + 2;
-  uint64_t* bar_pv = bar_s + 1;
+  // kv_full[s]: stage s of K and V (kSingle: [0] = K, [1] = V; PIPE: K of ring stage s, v_full[s] its V)
+  uint64_t* kv_full = reinterpret_cast<uint64_t*>(PIPE ? smem + 2 * kRing * kKVTile
+                                                       : p_tile + kTile + 2 * kStages * kKVTile);
+  uint64_t* v_full = kv_full + kRing;
+  uint64_t* bar_s = PIPE ? kv_full + 2 * kRing : kv_full + 2;  // PIPE: one per score buffer
+  uint64_t* bar_pv = PIPE ? bar_s + 2 : bar_s + 1;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bar_pv + 1);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
   // [4][128] row partials (kSingle: inside the P tile, free whenever the partials are in use)
-  float* red = kSingle ? reinterpret_cast<float*>(p_tile) : reinterpret_cast<float*>(reinterpret_cast<uint8_t*>(kv_full) + 64);
+  float* red = kSingle ? reinterpret_cast<float*>(p_tile)
+                       : reinterpret_cast<float*>(reinterpret_cast<uint8_t*>(kv_full) + (PIPE ? 128 : 64));
 
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int quad = warp & 3, quarter = warp >> 2;
   const int r = quad * 32 + lane;  // this thread's row (TMEM lane)
   unsigned long long* stamp = (trace != nullptr && tid == 0)
-                                  ? trace + (static_cast<size_t>(blockIdx.y) * gridDim.x + blockIdx.x) * 8
+                                  ? trace + (static_cast<size_t>(blockIdx.y) * gridDim.x + blockIdx.x) * 16
                                   : nullptr;
   if (stamp) stamp[0] = global_timer_ns();
   pdl_trigger();
@@ -354,6 +380,15 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
     for (int a = 0; a < kAtoms; ++a) tma_load_2d(dst + a * kAtom, is_v ? &tm_v : &tm_k, bar, 64 * a, y);
   };
+  // PIPE: K or V of chunk c into stage st, each on its own barrier
+  auto issue_half = [&](int c, int st, bool is_v) {
+    const int y = static_cast<int>(kv_row(pages, b, Hkv, kvh, S, c * kKeys));
+    uint64_t* bar = is_v ? &v_full[st] : &kv_full[st];
+    uint8_t* dst = (is_v ? v_tiles : k_tiles) + st * kKVTile;
+    mbar_arrive_expect_tx(bar, kAtoms * kAtom);
+#pragma unroll
+    for (int a = 0; a < kAtoms; ++a) tma_load_2d(dst + a * kAtom, is_v ? &tm_v : &tm_k, bar, 64 * a, y);
+  };
   // Chunks whose committed keys are all hidden by the keep bitmap (and that hold no new key) are skipped: the
   // CTA walks the active chunks only, every thread computing the same sequence from the bitmap.
   auto active = [&](int c) -> bool {
@@ -375,11 +410,25 @@ __global__ void __launch_bounds__(kThreads, 1)
     mbar_init(&kv_full[1], 1);
     mbar_init(bar_s, 1);
     mbar_init(bar_pv, 1);
+    if constexpr (PIPE) {
+      for (int st = 0; st < kRing; ++st) {
+        mbar_init(&kv_full[st], 1);
+        mbar_init(&v_full[st], 1);
+      }
+      mbar_init(bar_s + 1, 1);
+    }
     *abort_flag = 0;
     fence_mbar_init();
     // the first active K/V chunks stream while the CTA allocates TMEM and stages Q
     const int a0 = next_active(c0);
-    if constexpr (kSingle) {
+    if constexpr (PIPE) {  // the first kRing chunks fill both rings
+      int a = a0;
+      for (int j = 0; j < kRing && a < c1; ++j) {
+        issue_half(a, j, false);
+        issue_half(a, j, true);
+        a = next_active(a + 1);
+      }
+    } else if constexpr (kSingle) {
       if (a0 < c1) {
         issue_one(a0, false);
         issue_one(a0, true);
@@ -393,8 +442,28 @@ __global__ void __launch_bounds__(kThreads, 1)
   __syncwarp();
   if (warp == 0) tmem_alloc(tmem_slot, kTmemCols);
 
-  // Q row r, 16-byte chunks [quarter * D / 32, + D / 32) -> swizzled K-major tile (zeros for padding rows)
-  {
+  if constexpr (PIPE) {
+    // Q row r, dimensions [quarter * D / 4, + D / 4) -> TMEM lane r, packed two per column from column 256 + D
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tq = *tmem_slot + 256 + D + quarter * (D / 8) + (static_cast<uint32_t>(quad * 32) << 16);
+    const uint4* src = reinterpret_cast<const uint4*>(q + (static_cast<size_t>(b) * T + t) * H * D +
+                                                      static_cast<size_t>(head) * D);
+    uint32_t w[D / 8];
+#pragma unroll
+    for (int c = 0; c < D / 32; ++c) {
+      const uint4 v = row_valid ? src[quarter * (D / 32) + c] : make_uint4(0, 0, 0, 0);
+      w[4 * c] = v.x;
+      w[4 * c + 1] = v.y;
+      w[4 * c + 2] = v.z;
+      w[4 * c + 3] = v.w;
+    }
+    if constexpr (D == 128) tmem_st_u32x16(tq, w);
+    else tmem_st_u32x8(tq, w);
+    tmem_wait_st();
+  } else {
+    // Q row r, 16-byte chunks [quarter * D / 32, + D / 32) -> swizzled K-major tile (zeros for padding rows)
     const uint4* src = reinterpret_cast<const uint4*>(q + (static_cast<size_t>(b) * T + t) * H * D +
                                                       static_cast<size_t>(head) * D);
 #pragma unroll
@@ -421,147 +490,347 @@ __global__ void __launch_bounds__(kThreads, 1)
   constexpr uint32_t idesc_s = idesc_bf16_f32(kRows, kKeys);
   constexpr uint32_t idesc_pv = idesc_bf16_f32(kRows, D, /*b_mn_major=*/true);
   bool ok = true;
-
-  int c = next_active(c0);
-  int c_next = c < c1 ? next_active(c + 1) : c1;
-  for (int i = 0; c < c1 && ok; ++i) {
-    const int c_after = c_next < c1 ? next_active(c_next + 1) : c1;  // the chunk two ahead (prefetched below)
-    const int s = kSingle ? 0 : (i & 1);
-    const uint32_t kv_phase = kSingle ? (i & 1) : ((i >> 1) & 1);
-    const uint32_t ph = i & 1;
-    ok = mbar_wait(&kv_full[s], kv_phase, status, kStatusWaitFull, abort_flag);
-    if (!ok) break;
-    if (stamp && i == 0) stamp[2] = global_timer_ns();
-    if constexpr (FP8) {  // the previous chunk's S MMA has completed: the converted K tile is free
-      convert_fp8_tile(raw + s * 2 * kRawTile, k_tiles, tid);
-      fence_async_smem();
-      tc_fence_before();
-      __syncthreads();
-    } else if constexpr (!kSingle) {
-      if (c < q_chunks) {  // stage s was last read by chunk c - 2, whose MMAs have completed
-        const size_t chunk_id = (static_cast<size_t>(b) * Hkv + kvh) * (S / kKeys) + c;
-        dequant_kivi_tile(kivi + chunk_id * kivi_chunk_bytes(kivi_bits), kivi_bits, k_tiles + s * kKVTile,
-                          v_tiles + s * kKVTile, tid);
-        fence_async_smem();
-        tc_fence_before();
-        __syncthreads();
-      }
-    }
-    if (tid == 0) {
+  if constexpr (PIPE) {
+    const uint32_t tmem_o = tmem + 256 + ocol0;
+    const uint32_t tmem_q = tmem + 256 + D, tmem_p = tmem + 256 + D + D / 2;  // Q and P, two bf16 per column
+    // warps whose 32 rows are all padding (decode: T * G rows of the 128) skip the softmax and the O updates: their
+    // rows' P and O are never read back (an MMA row depends only on its own row of P)
+    const bool live = m_tile * kRows + quad * 32 < T * G;
+    // S of the chunk in K stage kst into score buffer sb (A = Q from TMEM), signalled on bar_s[sb]
+    auto issue_s = [&](int sb, int kst) {
       tc_fence_after();
-      const uint32_t qa = smem_u32(q_tile), ka = smem_u32(k_tiles + (FP8 ? 0 : s * kKVTile));
+      const uint32_t ka = smem_u32(k_tiles + kst * kKVTile);
 #pragma unroll
       for (int kk = 0; kk < D / 16; ++kk) {
         const uint32_t off = (kk >> 2) * kAtom + (kk & 3) * 32;
-        umma_bf16(tmem, desc_kmajor_sw128(qa + off), desc_kmajor_sw128(ka + off), idesc_s, kk != 0);
+        umma_bf16_ta(tmem + 128 * sb, tmem_q + kk * 8, desc_kmajor_sw128(ka + off), idesc_s, kk != 0);
       }
-      umma_commit(bar_s);
-    }
-    __syncwarp();
-    if constexpr (FP8) {  // V converts while the S MMA runs (the previous PV MMA has completed)
-      convert_fp8_tile(raw + s * 2 * kRawTile + kRawTile, v_tiles, tid);
-      fence_async_smem();
-    }
-    ok = mbar_wait(bar_s, ph, status, kStatusWaitAccum, abort_flag);
-    if (!ok) break;
-    __syncwarp();
-    tc_fence_after();
-    if constexpr (kSingle) {  // the S MMA has read K: the next chunk's K streams during this chunk's softmax and PV
-      if (tid == 0 && c_next < c1) issue_one(c_next, false);
-    }
-    if (stamp && i == 0) stamp[3] = global_timer_ns();
-
-    // this thread's 32 scores of the chunk
-    float sc[32];
-    tmem_ld16(tmem_s + lane_off, sc);
-    tmem_ld16(tmem_s + lane_off + 16, sc + 16);
-    const int s0 = c * kKeys + col0;
-    uint32_t vis = tail ? visible32(s0, tc_lim, 0, false, 0ull, 0, row_valid)
-                        : visible32(s0, base, nn, use_mask, bits, causal_lim, row_valid);
-    if (keep != nullptr) {  // evicted committed slots are invisible (new slots are never evicted)
-      const uint32_t kw = keep[(static_cast<size_t>(b) * Hkv + kvh) * (S / 32) + s0 / 32];
-      const int pre = min(max(base - s0, 0), 32);
-      const uint32_t committed = pre >= 32 ? 0xffffffffu : ((1u << pre) - 1u);
-      vis &= kw | ~committed;
-    }
-    if (opts.window > 0) vis &= at_or_above(s0, wlo);
-    float qmax = -INFINITY;
-    if (capped) {
-#pragma unroll
-      for (int j = 0; j < 32; ++j) sc[j] = cap_out * tanhf(sc[j] * cap_in);
-    } else {
-#pragma unroll
-      for (int j = 0; j < 32; ++j) sc[j] *= scale_log2;
-    }
-#pragma unroll
-    for (int j = 0; j < 32; ++j)
-      if ((vis >> j) & 1u) qmax = fmaxf(qmax, sc[j]);
-    red[quarter * kRows + r] = qmax;
-    __syncthreads();
-    const float cmax = fmaxf(fmaxf(red[r], red[kRows + r]), fmaxf(red[2 * kRows + r], red[3 * kRows + r]));
-    if constexpr (kSingle) __syncthreads();  // every thread has read the partials before P overwrites them
-    const float m_new = fmaxf(m_run, cmax);
-    const float alpha = m_new == -INFINITY ? 1.f : fast_exp2(m_run - m_new);
-    float csum = 0.f;
-    uint32_t packed[16];
-#pragma unroll
-    for (int j = 0; j < 32; j += 2) {
-      const float p0 = ((vis >> j) & 1u) ? fast_exp2(sc[j] - m_new) : 0.f;
-      const float p1 = ((vis >> (j + 1)) & 1u) ? fast_exp2(sc[j + 1] - m_new) : 0.f;
-      __nv_bfloat162 h2 = __floats2bfloat162_rn(p0, p1);
-      csum += __bfloat162float(h2.x) + __bfloat162float(h2.y);  // the sum of what P . V multiplies
-      packed[j / 2] = *reinterpret_cast<uint32_t*>(&h2);
-    }
-#pragma unroll
-    for (int u = 0; u < 4; ++u) {
-      store_row_swizzled(p_tile, r, quarter * 4 + u,
-                         make_uint4(packed[4 * u], packed[4 * u + 1], packed[4 * u + 2], packed[4 * u + 3]));
-    }
-    l_run = l_run * alpha + csum;
-    m_run = m_new;
-    if (stamp && i == 0) stamp[4] = global_timer_ns();
-    fence_async_smem();
-    tc_fence_before();
-    __syncthreads();
-    if constexpr (FP8) {  // every thread has converted stage s: its raw codes may be overwritten
-      if (tid == 0 && c_after < c1) issue_kv(c_after, s);
-    }
-    if constexpr (kSingle) {
-      ok = mbar_wait(&kv_full[1], ph, status, kStatusWaitFull, abort_flag);
-      if (!ok) break;
-    }
+      umma_commit(&bar_s[sb]);
+    };
+    int c = next_active(c0);
+    int c_next = c < c1 ? next_active(c + 1) : c1;
+    // thread 0's ring cursors: sequence index and chunk of the next K / V load (the prologue issued kRing of each)
+    int kq = 0, vq = 0, k_id = c, v_id = c, pv_done = -1;
     if (tid == 0) {
-      tc_fence_after();
-      const uint32_t pa = smem_u32(p_tile), va = smem_u32(v_tiles + (FP8 ? 0 : s * kKVTile));
-#pragma unroll
-      for (int kk = 0; kk < kKeys / 16; ++kk) {
-        const uint32_t a_off = (kk >> 2) * kAtom + (kk & 3) * 32;
-        umma_bf16(tmem + 128, desc_kmajor_sw128(pa + a_off), desc_mnmajor_sw128(va + kk * 2048, kAtom), idesc_pv,
-                  kk != 0);
+      while (kq < kRing && k_id < c1) {
+        k_id = next_active(k_id + 1);
+        ++kq;
       }
-      umma_commit(bar_pv);
+      vq = kq;
+      v_id = k_id;
+      if (c < c1) {
+        ok = mbar_wait(&kv_full[0], 0, status, kStatusWaitFull, abort_flag);
+        if (ok) issue_s(0, 0);
+      }
     }
-    __syncwarp();
-    ok = mbar_wait(bar_pv, ph, status, kStatusWaitAccum, abort_flag);
-    if (!ok) break;
-    __syncwarp();
-    tc_fence_after();
-    if (stamp && i == 0) stamp[5] = global_timer_ns();
-    if constexpr (kSingle) {  // the PV MMA has read V: the next chunk's V streams during its S and softmax
-      if (tid == 0 && c_next < c1) issue_one(c_next, true);
-    } else if constexpr (!FP8) {
-      if (tid == 0 && c_after < c1) issue_kv(c_after, s);  // both MMAs reading stage s are done
-    }
-    __syncwarp();
+    // V of sequence index j may load into stage j % kRing once P . V of j - kRing has completed
+    auto refill_v = [&]() {
+      while (vq <= pv_done + kRing && v_id < c1) {
+        issue_half(v_id, vq % kRing, true);
+        v_id = next_active(v_id + 1);
+        ++vq;
+      }
+    };
+    int i = 0;
+    for (; c < c1; ++i) {
+      const int sb = i & 1;
+      unsigned long long* fine = (stamp != nullptr && i == 2) ? stamp + 8 : nullptr;  // chunk 2, in SM cycles
+      if (fine) fine[0] = clock64();
+      ok = mbar_wait(&bar_s[sb], (i >> 1) & 1, status, kStatusWaitAccum, abort_flag);
+      if (!ok) break;
+      __syncwarp();
+      tc_fence_after();
+      if (stamp && i == 0) stamp[2] = global_timer_ns();
+      if (fine) fine[1] = clock64();
+      if (tid == 0) {
+        while (kq <= i + kRing && k_id < c1) {  // S of chunk i has read its K stage
+          issue_half(k_id, kq % kRing, false);
+          k_id = next_active(k_id + 1);
+          ++kq;
+        }
+        if (c_next < c1) {  // S of chunk i + 1 runs during this chunk's softmax
+          const int kst = (i + 1) % kRing;
+          ok = mbar_wait(&kv_full[kst], ((i + 1) / kRing) & 1, status, kStatusWaitFull, abort_flag);
+          if (ok) issue_s(sb ^ 1, kst);
+        }
+        if (i > 0 && pv_done < i - 1 && mbar_try_wait(bar_pv, (i - 1) & 1)) pv_done = i - 1;
+        refill_v();
+      }
+      __syncwarp();
+      if (fine) fine[2] = clock64();
+
+      float sc[32];
+      if (live) tmem_ld32(tmem + 128 * sb + col0 + lane_off, sc);
+      if (stamp && i == 0) stamp[3] = global_timer_ns();
+      const int s0 = c * kKeys + col0;
+      // Every row computes p = 2^(fma(s, scale log2(e), -m)) from its raw scores s and the maximum of its visible
+      // raw scores times the scale (equal to the maximum of the scaled ones), so whether a warp takes the
+      // all-visible fast path (no per-key tests) never changes a row's bits. Soft-capped scores are transformed
+      // first (cap log2(e) tanh(s scale / cap)) and then enter with a unit scale.
+      uint32_t vis = 0u;
+      float qmax = -INFINITY;
+      bool full = false;
+      const float sl = capped ? 1.f : scale_log2;
+      if (live) {
+        vis = tail ? visible32(s0, tc_lim, 0, false, 0ull, 0, row_valid)
+                   : visible32(s0, base, nn, use_mask, bits, causal_lim, row_valid);
+        if (keep != nullptr) {  // evicted committed slots are invisible (new slots are never evicted)
+          const uint32_t kw = keep[(static_cast<size_t>(b) * Hkv + kvh) * (S / 32) + s0 / 32];
+          const int pre = min(max(base - s0, 0), 32);
+          const uint32_t committed = pre >= 32 ? 0xffffffffu : ((1u << pre) - 1u);
+          vis &= kw | ~committed;
+        }
+        if (opts.window > 0) vis &= at_or_above(s0, wlo);
+        if (capped) {
 #pragma unroll
-    for (int c16 = 0; c16 < kDQ; c16 += 16) {  // 16 columns at a time keeps D = 256 within the register budget
-      float pv[16];
-      tmem_ld16(tmem_pv + lane_off + c16, pv);
+          for (int j = 0; j < 32; ++j) sc[j] = cap_out * tanhf(sc[j] * cap_in);
+        }
+        full = __all_sync(0xffffffffu, vis == 0xffffffffu);
+        float mx = -INFINITY;
+        if (full) {
 #pragma unroll
-      for (int d = 0; d < 16; ++d) o[c16 + d] = o[c16 + d] * alpha + pv[d];
+          for (int j = 0; j < 32; ++j) mx = fmaxf(mx, sc[j]);
+        } else {
+#pragma unroll
+          for (int j = 0; j < 32; ++j)
+            if ((vis >> j) & 1u) mx = fmaxf(mx, sc[j]);
+        }
+        qmax = mx * sl;
+        red[quarter * kRows + r] = qmax;
+      }
+      __syncthreads();
+      if (fine) fine[3] = clock64();
+      float alpha = 1.f, csum = 0.f;
+      uint32_t packed[16];
+      if (live) {
+        const float cmax = fmaxf(fmaxf(red[r], red[kRows + r]), fmaxf(red[2 * kRows + r], red[3 * kRows + r]));
+        // lazy rescaling: the reference maximum moves only when this chunk exceeds it by more than kLazyLog2
+        if (cmax > m_run + kLazyLog2 || (m_run == -INFINITY && cmax != -INFINITY)) {
+          alpha = m_run == -INFINITY ? 0.f : fast_exp2(m_run - cmax);
+          m_run = cmax;
+        }
+        const float nm = -m_run;
+        if (full) {
+#pragma unroll
+          for (int j = 0; j < 32; j += 2) {
+            const float p0 = fast_exp2(fmaf(sc[j], sl, nm)), p1 = fast_exp2(fmaf(sc[j + 1], sl, nm));
+            __nv_bfloat162 h2 = __floats2bfloat162_rn(p0, p1);
+            csum += p0 + p1;
+            packed[j / 2] = *reinterpret_cast<uint32_t*>(&h2);
+          }
+        } else {
+#pragma unroll
+          for (int j = 0; j < 32; j += 2) {
+            const float p0 = ((vis >> j) & 1u) ? fast_exp2(fmaf(sc[j], sl, nm)) : 0.f;
+            const float p1 = ((vis >> (j + 1)) & 1u) ? fast_exp2(fmaf(sc[j + 1], sl, nm)) : 0.f;
+            __nv_bfloat162 h2 = __floats2bfloat162_rn(p0, p1);
+            csum += p0 + p1;
+            packed[j / 2] = *reinterpret_cast<uint32_t*>(&h2);
+          }
+        }
+      }
+      l_run = l_run * alpha + csum;
+      if (i > 0) {  // P . V of chunk i - 1 has finished with the P tile and the accumulator
+        ok = mbar_wait(bar_pv, (i - 1) & 1, status, kStatusWaitAccum, abort_flag);
+        if (!ok) break;
+        __syncwarp();
+        tc_fence_after();
+        if (fine) fine[4] = clock64();
+        if (tid == 0) {
+          pv_done = i - 1;
+          refill_v();
+        }
+        if (live && __any_sync(0xffffffffu, alpha != 1.f)) {  // rows whose maximum moved: O *= alpha (others x 1)
+#pragma unroll
+          for (int c16 = 0; c16 < kDQ; c16 += 16) {
+            float ov[16];
+            tmem_ld16(tmem_o + lane_off + c16, ov);
+#pragma unroll
+            for (int d = 0; d < 16; ++d) ov[d] *= alpha;
+            tmem_st16(tmem_o + lane_off + c16, ov);
+          }
+        }
+      }
+      if (live) {  // this row's 32 probabilities: 16 columns of P from column 16 * quarter
+        tmem_st_u32x16(tmem_p + quarter * 16 + lane_off, packed);
+        tmem_wait_st();
+      }
+      if (stamp && i == 0) stamp[4] = global_timer_ns();
+      if (fine) fine[5] = clock64();
+      tc_fence_before();
+      __syncthreads();
+      if (fine) fine[6] = clock64();
+      if (tid == 0) {
+        const int vst = i % kRing;
+        ok = mbar_wait(&v_full[vst], (i / kRing) & 1, status, kStatusWaitFull, abort_flag);
+        if (ok) {
+          tc_fence_after();
+          const uint32_t va = smem_u32(v_tiles + vst * kKVTile);
+#pragma unroll
+          for (int kk = 0; kk < kKeys / 16; ++kk)
+            umma_bf16_ta(tmem + 256, tmem_p + kk * 8, desc_mnmajor_sw128(va + kk * 2048, kAtom), idesc_pv,
+                         i > 0 || kk != 0);
+          umma_commit(bar_pv);
+        }
+      }
+      __syncwarp();
+      if (stamp && i == 0) stamp[5] = global_timer_ns();
+      if (fine) fine[7] = clock64();
+      c = c_next;
+      c_next = c_next < c1 ? next_active(c_next + 1) : c1;
     }
-    c = c_next;
-    c_next = c_after;
+    // the last P . V, then the accumulator into registers for the epilogue
+    if (ok && i > 0 && mbar_wait(bar_pv, (i - 1) & 1, status, kStatusWaitAccum, abort_flag)) {
+      __syncwarp();
+      tc_fence_after();
+#pragma unroll
+      if (live) {
+        for (int c16 = 0; c16 < kDQ; c16 += 16) tmem_ld16(tmem_o + lane_off + c16, o + c16);
+      }
+    }
+  } else {
+
+    int c = next_active(c0);
+    int c_next = c < c1 ? next_active(c + 1) : c1;
+    for (int i = 0; c < c1 && ok; ++i) {
+      const int c_after = c_next < c1 ? next_active(c_next + 1) : c1;  // the chunk two ahead (prefetched below)
+      const int s = kSingle ? 0 : (i & 1);
+      const uint32_t kv_phase = kSingle ? (i & 1) : ((i >> 1) & 1);
+      const uint32_t ph = i & 1;
+      ok = mbar_wait(&kv_full[s], kv_phase, status, kStatusWaitFull, abort_flag);
+      if (!ok) break;
+      if (stamp && i == 0) stamp[2] = global_timer_ns();
+      if constexpr (FP8) {  // the previous chunk's S MMA has completed: the converted K tile is free
+        convert_fp8_tile(raw + s * 2 * kRawTile, k_tiles, tid);
+        fence_async_smem();
+        tc_fence_before();
+        __syncthreads();
+      } else if constexpr (!kSingle) {
+        if (c < q_chunks) {  // stage s was last read by chunk c - 2, whose MMAs have completed
+          const size_t chunk_id = (static_cast<size_t>(b) * Hkv + kvh) * (S / kKeys) + c;
+          dequant_kivi_tile(kivi + chunk_id * kivi_chunk_bytes(kivi_bits), kivi_bits, k_tiles + s * kKVTile,
+                            v_tiles + s * kKVTile, tid);
+          fence_async_smem();
+          tc_fence_before();
+          __syncthreads();
+        }
+      }
+      if (tid == 0) {
+        tc_fence_after();
+        const uint32_t qa = smem_u32(q_tile), ka = smem_u32(k_tiles + (FP8 ? 0 : s * kKVTile));
+#pragma unroll
+        for (int kk = 0; kk < D / 16; ++kk) {
+          const uint32_t off = (kk >> 2) * kAtom + (kk & 3) * 32;
+          umma_bf16(tmem, desc_kmajor_sw128(qa + off), desc_kmajor_sw128(ka + off), idesc_s, kk != 0);
+        }
+        umma_commit(bar_s);
+      }
+      __syncwarp();
+      if constexpr (FP8) {  // V converts while the S MMA runs (the previous PV MMA has completed)
+        convert_fp8_tile(raw + s * 2 * kRawTile + kRawTile, v_tiles, tid);
+        fence_async_smem();
+      }
+      ok = mbar_wait(bar_s, ph, status, kStatusWaitAccum, abort_flag);
+      if (!ok) break;
+      __syncwarp();
+      tc_fence_after();
+      if constexpr (kSingle) {  // the S MMA has read K: the next chunk's K streams during this chunk's softmax and PV
+        if (tid == 0 && c_next < c1) issue_one(c_next, false);
+      }
+      if (stamp && i == 0) stamp[3] = global_timer_ns();
+
+      // this thread's 32 scores of the chunk
+      float sc[32];
+      tmem_ld16(tmem_s + lane_off, sc);
+      tmem_ld16(tmem_s + lane_off + 16, sc + 16);
+      const int s0 = c * kKeys + col0;
+      uint32_t vis = tail ? visible32(s0, tc_lim, 0, false, 0ull, 0, row_valid)
+                          : visible32(s0, base, nn, use_mask, bits, causal_lim, row_valid);
+      if (keep != nullptr) {  // evicted committed slots are invisible (new slots are never evicted)
+        const uint32_t kw = keep[(static_cast<size_t>(b) * Hkv + kvh) * (S / 32) + s0 / 32];
+        const int pre = min(max(base - s0, 0), 32);
+        const uint32_t committed = pre >= 32 ? 0xffffffffu : ((1u << pre) - 1u);
+        vis &= kw | ~committed;
+      }
+      if (opts.window > 0) vis &= at_or_above(s0, wlo);
+      float qmax = -INFINITY;
+      if (capped) {
+#pragma unroll
+        for (int j = 0; j < 32; ++j) sc[j] = cap_out * tanhf(sc[j] * cap_in);
+      } else {
+#pragma unroll
+        for (int j = 0; j < 32; ++j) sc[j] *= scale_log2;
+      }
+#pragma unroll
+      for (int j = 0; j < 32; ++j)
+        if ((vis >> j) & 1u) qmax = fmaxf(qmax, sc[j]);
+      red[quarter * kRows + r] = qmax;
+      __syncthreads();
+      const float cmax = fmaxf(fmaxf(red[r], red[kRows + r]), fmaxf(red[2 * kRows + r], red[3 * kRows + r]));
+      if constexpr (kSingle) __syncthreads();  // every thread has read the partials before P overwrites them
+      const float m_new = fmaxf(m_run, cmax);
+      const float alpha = m_new == -INFINITY ? 1.f : fast_exp2(m_run - m_new);
+      float csum = 0.f;
+      uint32_t packed[16];
+#pragma unroll
+      for (int j = 0; j < 32; j += 2) {
+        const float p0 = ((vis >> j) & 1u) ? fast_exp2(sc[j] - m_new) : 0.f;
+        const float p1 = ((vis >> (j + 1)) & 1u) ? fast_exp2(sc[j + 1] - m_new) : 0.f;
+        __nv_bfloat162 h2 = __floats2bfloat162_rn(p0, p1);
+        csum += __bfloat162float(h2.x) + __bfloat162float(h2.y);  // the sum of what P . V multiplies
+        packed[j / 2] = *reinterpret_cast<uint32_t*>(&h2);
+      }
+#pragma unroll
+      for (int u = 0; u < 4; ++u) {
+        store_row_swizzled(p_tile, r, quarter * 4 + u,
+                           make_uint4(packed[4 * u], packed[4 * u + 1], packed[4 * u + 2], packed[4 * u + 3]));
+      }
+      l_run = l_run * alpha + csum;
+      m_run = m_new;
+      if (stamp && i == 0) stamp[4] = global_timer_ns();
+      fence_async_smem();
+      tc_fence_before();
+      __syncthreads();
+      if constexpr (FP8) {  // every thread has converted stage s: its raw codes may be overwritten
+        if (tid == 0 && c_after < c1) issue_kv(c_after, s);
+      }
+      if constexpr (kSingle) {
+        ok = mbar_wait(&kv_full[1], ph, status, kStatusWaitFull, abort_flag);
+        if (!ok) break;
+      }
+      if (tid == 0) {
+        tc_fence_after();
+        const uint32_t pa = smem_u32(p_tile), va = smem_u32(v_tiles + (FP8 ? 0 : s * kKVTile));
+#pragma unroll
+        for (int kk = 0; kk < kKeys / 16; ++kk) {
+          const uint32_t a_off = (kk >> 2) * kAtom + (kk & 3) * 32;
+          umma_bf16(tmem + 128, desc_kmajor_sw128(pa + a_off), desc_mnmajor_sw128(va + kk * 2048, kAtom), idesc_pv,
+                    kk != 0);
+        }
+        umma_commit(bar_pv);
+      }
+      __syncwarp();
+      ok = mbar_wait(bar_pv, ph, status, kStatusWaitAccum, abort_flag);
+      if (!ok) break;
+      __syncwarp();
+      tc_fence_after();
+      if (stamp && i == 0) stamp[5] = global_timer_ns();
+      if constexpr (kSingle) {  // the PV MMA has read V: the next chunk's V streams during its S and softmax
+        if (tid == 0 && c_next < c1) issue_one(c_next, true);
+      } else if constexpr (!FP8) {
+        if (tid == 0 && c_after < c1) issue_kv(c_after, s);  // both MMAs reading stage s are done
+      }
+      __syncwarp();
+#pragma unroll
+      for (int c16 = 0; c16 < kDQ; c16 += 16) {  // 16 columns at a time keeps D = 256 within the register budget
+        float pv[16];
+        tmem_ld16(tmem_pv + lane_off + c16, pv);
+#pragma unroll
+        for (int d = 0; d < 16; ++d) o[c16 + d] = o[c16 + d] * alpha + pv[d];
+      }
+      c = c_next;
+      c_next = c_after;
+    }
   }
   if (stamp) stamp[6] = global_timer_ns();
   tc_fence_before();
@@ -1004,7 +1273,9 @@ AttnPlan attention_plan(int B, int T, int H, int Hkv, int S, int num_sms, bool t
   const int span = window > 0 ? std::min(total_chunks, (window + 2 * kKeys - 1) / kKeys + 1) : total_chunks;
   const int heads = B * Hkv;
   int splits = 1;
-  if (heads < num_sms) splits = std::min(span, std::max(1, (2 * num_sms) / heads));
+  // one wave of splits per (row, KV head) for a decode pass; the split count never depends on T, so a tree pass and
+  // a one-token pass reduce a row's keys in the same groups (the exact-tail guarantee)
+  if (heads < num_sms) splits = std::min(span, std::max(1, num_sms / heads));
   plan.chunks_per_split = (span + splits - 1) / splits;
   plan.splits = (span + plan.chunks_per_split - 1) / plan.chunks_per_split;
   if (span < total_chunks)
@@ -1046,10 +1317,24 @@ int launch_attention(const void* q, const CUtensorMap* tm_k, const CUtensorMap* 
                plan.chunks_per_split, plan.m_tiles, status, trace, k_scale, v_scale, keep, lse_out, kivi, kivi_chunks,
                kivi_bits, tail_w, opts, pages);
   };
-  if (D == 64) run(attn_tc_kernel<false, 64>, attn_smem_bytes(64));
-  else if (D == 256) run(attn_tc_kernel<false, 256>, attn_smem_bytes(256));
-  else if (fp8) run(attn_tc_kernel<true, 128>, kSmem);
-  else run(attn_tc_kernel<false, 128>, kSmem);
+  // bf16 caches without KIVI codes take the pipelined walk (ECZ_ATTN_PIPE=0 selects the serial one, for comparison)
+  static const bool pipe_env = [] {
+    const char* v = std::getenv("ECZ_ATTN_PIPE");
+    return v == nullptr || v[0] != '0';
+  }();
+  const bool pipe = pipe_env && kivi == nullptr;
+  if (D == 64) {
+    if (pipe) run(attn_tc_kernel<false, 64, true>, attn_pipe_smem_bytes(64));
+    else run(attn_tc_kernel<false, 64>, attn_smem_bytes(64));
+  } else if (D == 256) {
+    run(attn_tc_kernel<false, 256>, attn_smem_bytes(256));
+  } else if (fp8) {
+    run(attn_tc_kernel<true, 128>, kSmem);
+  } else if (pipe) {
+    run(attn_tc_kernel<false, 128, true>, attn_pipe_smem_bytes(128));
+  } else {
+    run(attn_tc_kernel<false, 128>, kSmem);
+  }
   dim3 mgrid(ctas, kRows / 4);
   if (tail_w > 0) {
     auto merge = D == 64 ? attn_merge_tail_kernel<64> : D == 256 ? attn_merge_tail_kernel<256>

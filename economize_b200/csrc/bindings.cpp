@@ -375,6 +375,12 @@ Tensor attention(Tensor q, Tensor k_cache, Tensor v_cache, Tensor kv_len, Tensor
   TORCH_CHECK(k_cache.size(3) == D && v_cache.size(3) == D, "attention: caches must have q's head_dim");
   const ecz::AttnPlan plan = ecz::attention_plan(B, T, H, Hkv, S, num_sms(q.get_device()), tail > 0, D,
                                                  static_cast<int>(window));
+  if (trace.has_value()) {  // sixteen int64 stamps per CTA
+    CHECK_ON(*trace, q);
+    TORCH_CHECK(trace->scalar_type() == at::kLong && trace->is_contiguous() &&
+                    trace->numel() >= static_cast<int64_t>(B) * Hkv * plan.m_tiles * plan.splits * 16,
+                "attention: trace must be a contiguous int64 tensor of at least 16 stamps per CTA");
+  }
   ecz::AttnOpts opts;
   opts.softcap = static_cast<float>(softcap);
   opts.sinks = sinks.has_value() ? sinks->data_ptr<float>() : nullptr;

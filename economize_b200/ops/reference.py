@@ -212,6 +212,17 @@ def clamped_swiglu(gate_up: torch.Tensor, limit: float = 7.0) -> torch.Tensor:
     return (up + 1) * (gate * torch.sigmoid(gate * 1.702))
 
 
+def glu(gate_up: torch.Tensor, act: str = "silu", limit: float = 7.0) -> torch.Tensor:
+    """The gated activations of :func:`economize_b200.ops.glu` in plain PyTorch (any device and dtype)."""
+    if act == "silu":
+        return silu_mul(gate_up)
+    if act == "gelu_tanh":
+        return gelu_tanh_mul(gate_up)
+    if act == "clamped_swiglu":
+        return clamped_swiglu(gate_up, limit)
+    raise ValueError(f"unsupported gated activation {act!r}")
+
+
 def linear(x: torch.Tensor, weight: torch.Tensor, bias: torch.Tensor | None = None) -> torch.Tensor:
     return F.linear(x, weight, bias)
 

@@ -27,6 +27,7 @@ import torch.nn.functional as F
 
 from .. import ops
 from ..errors import CommTimeoutError, ConfigError
+from ..ops import reference
 
 __all__ = ["ExpertParallel", "FusedExpertParallel", "moe_mlp", "moe_reference", "route", "shard_experts"]
 
@@ -58,7 +59,7 @@ def moe_reference(x: torch.Tensor, router: torch.Tensor, w_gate_up: torch.Tensor
         if rows.numel() == 0:
             continue
         gu = F.linear(x2[rows], w_gate_up[e], None if b_gate_up is None else b_gate_up[e])
-        y = F.linear(ops.glu(gu, act, limit), w_down[e], None if b_down is None else b_down[e])
+        y = F.linear(reference.glu(gu, act, limit), w_down[e], None if b_down is None else b_down[e])
         out.index_add_(0, rows, y.float() * w[rows, slot][:, None])
     return out.to(x.dtype).reshape(shape)
 

@@ -191,6 +191,22 @@ def dense_linear(x: torch.Tensor, w, b: torch.Tensor | None = None) -> torch.Ten
     return F.linear(x, w, b)
 
 
+def _check_plain_block(config) -> None:
+    """Refuse the block variants :func:`torch_block` does not model (it is the Llama block: pre-norms, per-head q/k
+    norms, causal attention over the whole row, a dense SwiGLU MLP)."""
+    variants = {"MoE MLPs": config.is_moe, "sandwich norms": config.sandwich_norm, "post norms": config.post_norm,
+                "full-width q/k norms": config.qk_norm_full, "NoPE layers": bool(config.nope_layers),
+                "sliding windows": any(config.window_of(i) for i in range(config.num_layers)),
+                "soft-caps": bool(config.attn_softcap), "sink logits": config.attn_sinks,
+                "an output-projection bias": config.o_bias, "a non-SwiGLU activation": config.hidden_act != "silu",
+                "scaled attention or residuals": config.attention_multiplier is not None
+                or config.residual_multiplier != 1.0}
+    found = [name for name, present in variants.items() if present]
+    if found:
+        raise ConfigError(f"the PyTorch training block models the Llama block; {config.model_type} has "
+                          f"{', '.join(found)}")
+
+
 def torch_block(layer, h: torch.Tensor, config, cos: torch.Tensor, sin: torch.Tensor) -> torch.Tensor:
     """A pre-norm decoder block in plain PyTorch (autograd, causal attention over the whole row): the residual
     stream ``h [B, S, H]`` in, the block's output stream out. Used to train technique-owned blocks and adapters."""
@@ -199,7 +215,7 @@ def torch_block(layer, h: torch.Tensor, config, cos: torch.Tensor, sin: torch.Te
     from ..ops.reference import rmsnorm
 
     lin = dense_linear
-
+    _check_plain_block(config)
     eps = config.rms_norm_eps
     batch, length, _ = h.shape
     heads, kv_heads, hd = config.num_heads, config.num_kv_heads, config.head_dim
