@@ -8,12 +8,18 @@ the warm-up generation (the case a launch-list capture profiles). ``--breakdown`
 the PyTorch profiler (CUPTI kernel records, graph replays included) and prints device microseconds and launches per
 cycle for every kernel name; run it with ``ECZ_PDL=0`` so that no kernel's record includes the time it waits for its
 predecessor (with programmatic dependent launch a kernel starts before the previous one ends).
+
+Under ``torchrun --nproc-per-node N`` (``WORLD_SIZE`` > 1) the target is sharded over the N ranks with tensor
+parallelism (the fused NVLink collectives; ``--nccl-tp`` for NCCL), every rank decodes the same prompts, the times
+are the maximum over the ranks and rank 0 prints (the breakdown is rank 0's kernels).
 """
 
 from __future__ import annotations
 
 import argparse
+import datetime
 import json
+import os
 
 import torch
 
@@ -36,12 +42,25 @@ def main(argv: list[str] | None = None) -> None:
     p.add_argument("--cycles-only", action="store_true")
     p.add_argument("--breakdown", type=int, default=0, metavar="N",
                    help="print the N kernels with the most device time per cycle (PyTorch profiler)")
+    p.add_argument("--nccl-tp", action="store_true", help="tensor parallelism over NCCL instead of the fused kernels")
     a = p.parse_args(argv)
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    if world > 1:
+        import torch.distributed as dist
+
+        torch.cuda.set_device(int(os.environ.get("LOCAL_RANK", rank)))
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300),
+                                device_id=torch.device("cuda", torch.cuda.current_device()))
     cfg = llama31_8b()
     cfg.num_layers = a.layers
     target = init_weights(CausalLM(cfg, torch.bfloat16, "cuda"), seed=0)
     eff = eco.apply(target, Eagle3Config(draft_vocab=32000))
     eff.techniques["eagle3"].reset_parameters(seed=0, identity=True)
+    if world > 1:
+        from economize_b200.distributed import TPGroup, tensor_parallel
+
+        tensor_parallel(eff.model, TPGroup(rank, world), fused=not a.nccl_tp)
     if a.mode == "tree":
         dc = eco.DecodeConfig(cycle_length=7, draft_policy="dynamic_tree", cuda_graphs=True,
                               draft_policy_options={"depth": 6, "topk": 10, "total_tokens": 60})
@@ -64,6 +83,8 @@ def main(argv: list[str] | None = None) -> None:
         return
     times, cycles = [], 0
     for _ in range(a.iters):
+        if world > 1:
+            dist.barrier()
         s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         s.record()
         res = eff.decode_batch(prompts, a.new_tokens, decoding=dc)
@@ -72,17 +93,36 @@ def main(argv: list[str] | None = None) -> None:
         times.append(s.elapsed_time(e))
     cycles = max(int(r.cycles) for r in res)
     ms = min(times)
+    if world > 1:
+        t = torch.tensor([ms], device="cuda")
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms = float(t.item())
     tokens = sum(int(r.tokens.numel()) for r in res)
     if a.breakdown:
-        _breakdown(eff, prompts, a.new_tokens, dc, a.breakdown)
-    print(json.dumps({"mode": a.mode, "batch": a.batch, "prompt_len": a.prompt_len, "new_tokens": a.new_tokens,
-                      "layers": a.layers, "ms_per_generate": round(ms, 2), "cycles": cycles,
-                      "ms_per_cycle_incl_prefill": round(ms / max(cycles, 1), 3),
-                      "tokens_per_s": round(tokens / ms * 1e3, 1),
-                      "mean_accepted": round(sum(r.mean_accepted for r in res) / len(res), 3)}))
+        _breakdown(eff, prompts, a.new_tokens, dc, a.breakdown, verbose=rank == 0)
+    if rank == 0:
+        print(json.dumps({"mode": a.mode, "batch": a.batch, "prompt_len": a.prompt_len,
+                          "new_tokens": a.new_tokens, "layers": a.layers, "tp": world,
+                          "ms_per_generate": round(ms, 2), "cycles": cycles,
+                          "ms_per_cycle_incl_prefill": round(ms / max(cycles, 1), 3),
+                          "tokens_per_s": round(tokens / ms * 1e3, 1),
+                          "mean_accepted": round(sum(r.mean_accepted for r in res) / len(res), 3)}))
+    if world > 1:  # release the captured graphs and the NVLink buffers before the group goes away
+        eff.refresh()
+        tpg = eff.model.tp
+        for runtime in (getattr(tpg, "comm", None), getattr(tpg, "sp", None)):
+            if runtime is not None:
+                runtime.close()
+        del eff, res
+        import gc
+
+        gc.collect()
+        torch.cuda.synchronize()
+        dist.barrier()
+        dist.destroy_process_group()
 
 
-def _breakdown(eff, prompts, new_tokens: int, dc, top: int) -> None:
+def _breakdown(eff, prompts, new_tokens: int, dc, top: int, verbose: bool = True) -> None:
     from torch.profiler import ProfilerActivity, profile
 
     engine = eff.decoder(dc)
@@ -98,6 +138,8 @@ def _breakdown(eff, prompts, new_tokens: int, dc, top: int) -> None:
             rows.append((t, e.count, e.key))
     rows.sort(reverse=True)
     total = sum(r[0] for r in rows)
+    if not verbose:
+        return
     print(json.dumps({"cycles": cycles, "kernel_us_per_cycle": round(total / cycles, 1),
                       "launches_per_cycle": round(sum(r[1] for r in rows) / cycles, 1)}))
     for t, n, name in rows[:top]:

@@ -149,17 +149,18 @@ def bench_attention(a) -> None:
     n_new = torch.full((B,), T, dtype=torch.int32, device=dev)
     parents = torch.arange(-1, T - 1, device=dev)[None].expand(B, T)  # a chain (worst case: full depth)
     mask = ancestor_bits(parents.contiguous(), T) if T > 1 else None
+    tail = a.tail if T <= 64 else 0
     if a.once:
-        ops.attention(q, k, v, kv_len, n_new, mask)
+        ops.attention(q, k, v, kv_len, n_new, mask, tail=tail)
         torch.cuda.synchronize()
         return
     if a.trace:
         _attention_timeline(q, k, v, kv_len, n_new, mask, a)
         return
-    ours = time_graph([lambda: ops.attention(q, k, v, kv_len, n_new, mask)] * 8, a.iters, a.warmup)
+    ours = time_graph([lambda: ops.attention(q, k, v, kv_len, n_new, mask, tail=tail)] * 8, a.iters, a.warmup)
     nbytes = 2 * (2 * B * Hkv * (a.ctx + T) * D + 2 * B * T * H * D)
     flops = 4 * B * T * H * (a.ctx + T) * D
-    _report("attention", {"B": B, "T": T, "H": H, "Hkv": Hkv, "ctx": a.ctx}, ours, nbytes, flops)
+    _report("attention", {"B": B, "T": T, "H": H, "Hkv": Hkv, "ctx": a.ctx, "tail": tail}, ours, nbytes, flops)
 
 
 def _steady_phases(st, med) -> dict:
@@ -333,6 +334,7 @@ def main(argv: list[str] | None = None) -> None:
     p.add_argument("--iters", type=int, default=20)
     p.add_argument("--warmup", type=int, default=3)
     p.add_argument("--once", action="store_true", help="one untimed call (for profiler captures)")
+    p.add_argument("--tail", type=int, default=0, help="attention: exact-tail width (decode passes use 16)")
     p.add_argument("--trace", action="store_true", help="attention: per-CTA phase timeline from the kernel's stamps")
     a = p.parse_args(argv)
     {"gemm": bench_gemm, "gemm_sweep": bench_gemm_sweep, "gemm_wq": bench_gemm_wq, "attention": bench_attention, "layer": bench_layer,

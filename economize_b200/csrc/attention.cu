@@ -683,8 +683,8 @@ __global__ void __launch_bounds__(kThreads, 1)
     if (ok && i > 0 && mbar_wait(bar_pv, (i - 1) & 1, status, kStatusWaitAccum, abort_flag)) {
       __syncwarp();
       tc_fence_after();
-#pragma unroll
       if (live) {
+#pragma unroll
         for (int c16 = 0; c16 < kDQ; c16 += 16) tmem_ld16(tmem_o + lane_off + c16, o + c16);
       }
     }
@@ -922,18 +922,14 @@ __device__ __forceinline__ void load_kv(const uint8_t* base, size_t row, int lan
   }
 }
 
-template <int E>
-__device__ __forceinline__ float tail_score(const float* qv, const float* kv, float scale_log2, float cap_in,
-                                           float cap_out) {
-  float d = qv[0] * kv[0];
-#pragma unroll
-  for (int e = 1; e < E; ++e) d = fmaf(qv[e], kv[e], d);
-  const float raw = warp_sum(d);
-  return cap_out > 0.f ? cap_out * tanhf(raw * cap_in) : raw * scale_log2;
-}
-
 constexpr int kTailKeysMax = 128;  // committed tail (tail_w <= 64) + new keys (at most 64)
 constexpr int kTailBatch = 8;      // keys whose loads are issued together
+
+// Shared memory of the tail merge: the K rows, then the V rows, of the slots [start, end) the CTA's four rows need
+// (at most tail_w committed slots below the shallowest row's position and the pass's 64 new slots).
+__host__ __device__ constexpr int tail_stage_bytes(int D, bool fp8, int tail_w) {
+  return 2 * (tail_w + 64) * (fp8 ? D : 2 * D);
+}
 
 template <int D>
 __global__ void __launch_bounds__(128) attn_merge_tail_kernel(
@@ -944,8 +940,10 @@ __global__ void __launch_bounds__(128) attn_merge_tail_kernel(
     int tail_w, const float* __restrict__ k_scale, const float* __restrict__ v_scale,
     const uint32_t* __restrict__ keep, float softcap, const float* __restrict__ sinks, KVPages pages,
     unsigned* status) {
-  __shared__ int s_row[4][kTailKeysMax];    // cache rows of this warp's tail keys, in position order
+  extern __shared__ __align__(16) uint8_t tail_stage[];  // K rows, then V rows, of slots [start, end)
+  __shared__ int s_row[4][kTailKeysMax];    // staged row of each of this warp's tail keys, in position order
   __shared__ float s_sc[4][kTailKeysMax];   // their scaled scores
+  __shared__ int s_lo[4], s_hi[4];
   pdl_trigger();
   pdl_wait();
   const int wid = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -955,7 +953,7 @@ __global__ void __launch_bounds__(128) attn_merge_tail_kernel(
   const int G = H / Hkv;
   const int p = m_tile * kRows + r;
   const int t = p / G;
-  if (t >= T) return;
+  const bool valid = t < T;
   const int head = kvh * G + p % G;
   const bool fp8 = k_scale != nullptr;
   const float sl = fp8 ? scale_log2 * k_scale[kvh] : scale_log2;
@@ -964,13 +962,48 @@ __global__ void __launch_bounds__(128) attn_merge_tail_kernel(
   const float cap_out = softcap > 0.f ? softcap * 1.4426950408889634f : 0.f;
   const int base = kv_len[b], nn = n_new[b];
   const bool use_mask = mask != nullptr;
-  const uint64_t bits = use_mask ? static_cast<uint64_t>(mask[static_cast<size_t>(b) * T + t]) : 0ull;
+  const uint64_t bits = (use_mask && valid) ? static_cast<uint64_t>(mask[static_cast<size_t>(b) * T + t]) : 0ull;
   const int depth = max(0, use_mask ? (__popcll(bits) - 1) : (q_offset + t));  // a row seeing no new key: 0
   const int lo = max(0, base + depth - tail_w);
   constexpr int E = D / 32;
+  const int n_end = min(nn, use_mask ? 64 : q_offset + t + 1);
+
+  // The four rows' slots [start, end) are staged once with 16-byte loads that are all in flight together (the
+  // rows of one token share them: a GQA group's heads are consecutive packed rows).
+  if (lane == 0) {
+    s_lo[wid] = valid ? min(lo, base) : INT_MAX;
+    s_hi[wid] = valid ? base + max(n_end, 0) : INT_MIN;
+  }
+  __syncthreads();
+  const int start = min(min(s_lo[0], s_lo[1]), min(s_lo[2], s_lo[3]));
+  const int end = max(max(s_hi[0], s_hi[1]), max(s_hi[2], s_hi[3]));
+  int rows = end > start ? end - start : 0;
+  // never stage past the buffer (a range this wide cannot come from kv_len / n_new of a valid pass); bounds-checked
+  // builds also report slots outside the cache
+  if (rows > tail_w + 64) rows = 0;
+  if (!index_ok(start >= 0 && end <= S, threadIdx.x == 0 ? status : nullptr)) rows = 0;
+  const int rb = fp8 ? D : 2 * D;  // bytes of one cache row
+  uint8_t* k_stage = tail_stage;
+  uint8_t* v_stage = tail_stage + (tail_w + 64) * rb;
+  {
+    const int per_row = rb / 16;
+    for (int i = threadIdx.x; i < rows * per_row; i += blockDim.x) {
+      const int row = i / per_row, c = i - row * per_row;
+      const size_t src = kv_row(pages, b, Hkv, kvh, S, start + row) * rb + c * 16;
+      const uint4 kx = __ldg(reinterpret_cast<const uint4*>(k_cache + src));
+      const uint4 vx = __ldg(reinterpret_cast<const uint4*>(v_cache + src));
+      *reinterpret_cast<uint4*>(k_stage + row * rb + c * 16) = kx;
+      *reinterpret_cast<uint4*>(v_stage + row * rb + c * 16) = vx;
+    }
+  }
+  __syncthreads();
+  if (!valid) return;
+  // this row's split partials: O of split sp, then its (max, sum)
+  auto part_o = [&](int sp) { return ws_o + ((static_cast<size_t>(tile) * splits + sp) * kRows + r) * D; };
+  auto part_ml = [&](int sp) { return ws_ml + ((static_cast<size_t>(tile) * splits + sp) * kRows + r) * 2; };
+
   float qv[E];
   load_kv<E>(reinterpret_cast<const uint8_t*>(q), (static_cast<size_t>(b) * T + t) * H + head, lane, false, qv);
-  const int n_end = min(nn, use_mask ? 64 : q_offset + t + 1);
 
   // the tail keys in position order: committed slots [lo, base) the keep bitmap shows, then the row's own new keys
   // (ancestors and itself, in depth order), compacted with warp ballots
@@ -981,45 +1014,72 @@ __global__ void __launch_bounds__(128) attn_merge_tail_kernel(
     if (vis && keep != nullptr)
       vis = (keep[(static_cast<size_t>(b) * Hkv + kvh) * (S / 32) + s / 32] >> (s & 31)) & 1u;
     const unsigned ballot = __ballot_sync(0xffffffffu, vis);
-    if (vis) s_row[wid][n_keys + __popc(ballot & ((1u << lane) - 1u))] = static_cast<int>(s);
+    if (vis) s_row[wid][n_keys + __popc(ballot & ((1u << lane) - 1u))] = s - start;
     n_keys += __popc(ballot);
   }
   for (int j0 = 0; j0 < n_end; j0 += 32) {
     const int j = j0 + lane;
     const bool vis = j < n_end && (use_mask ? ((bits >> j) & 1ull) != 0ull : j <= q_offset + t);
     const unsigned ballot = __ballot_sync(0xffffffffu, vis);
-    if (vis) s_row[wid][n_keys + __popc(ballot & ((1u << lane) - 1u))] = base + j;
+    if (vis) s_row[wid][n_keys + __popc(ballot & ((1u << lane) - 1u))] = base + j - start;
     n_keys += __popc(ballot);
   }
+  if (rows == 0) n_keys = 0;  // a failed bounds check staged nothing
   __syncwarp();
-  if constexpr (kCheckedBuild) {  // tail slots come from kv_len / n_new on the device
-    bool bad = false;
-    for (int i = lane; i < n_keys; i += 32) bad |= !(s_row[wid][i] >= 0 && s_row[wid][i] < S);
-    if (!index_ok(!__any_sync(0xffffffffu, bad), lane == 0 ? status : nullptr)) n_keys = 0;
-  }
 
-  // scores, batches of kTailBatch keys whose K loads are in flight together
+  // scores of kTailBatch keys at a time: each lane's partial dot products, then one butterfly that reduces the
+  // eight sums together (after the xor-16, -8 and -4 steps a lane keeps the key of its lane bits 4..2, and each step
+  // adds the same pairs warp_sum adds, so every score has warp_sum's bits)
+  static_assert(kTailBatch == 8, "the transposed reduction sums eight keys");
   float mx = -INFINITY;
   for (int sp = 0; sp < splits; ++sp) {
-    const size_t slot = (static_cast<size_t>(tile) * splits + sp) * kRows + r;
-    if (ws_ml[slot * 2 + 1] > 0.f) mx = fmaxf(mx, ws_ml[slot * 2]);
+    const float* ml = part_ml(sp);
+    if (ml[1] > 0.f) mx = fmaxf(mx, ml[0]);
   }
   const float sink2 = sinks != nullptr ? sinks[head] * 1.4426950408889634f : -INFINITY;
   mx = fmaxf(mx, sink2);
+  float kmx = -INFINITY;  // the tail keys' maximum (one lane per key of each batch)
   for (int i0 = 0; i0 < n_keys; i0 += kTailBatch) {
-    float kv[kTailBatch][E];
-#pragma unroll
-    for (int u = 0; u < kTailBatch; ++u)
-      if (i0 + u < n_keys) load_kv<E>(k_cache, kv_row(pages, b, Hkv, kvh, S, s_row[wid][i0 + u]), lane, fp8, kv[u]);
+    float d[kTailBatch];
 #pragma unroll
     for (int u = 0; u < kTailBatch; ++u) {
+      d[u] = 0.f;
       if (i0 + u < n_keys) {
-        const float sc = tail_score<E>(qv, kv[u], sl, cap_in, cap_out);
-        if (lane == 0) s_sc[wid][i0 + u] = sc;
-        mx = fmaxf(mx, sc);
+        float kv[E];
+        load_kv<E>(k_stage, s_row[wid][i0 + u], lane, fp8, kv);
+        float x = qv[0] * kv[0];
+#pragma unroll
+        for (int e = 1; e < E; ++e) x = fmaf(qv[e], kv[e], x);
+        d[u] = x;
       }
     }
+    float h4[4], h2[2];
+    const bool b4 = lane & 16, b3 = lane & 8, b2 = lane & 4;
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const float mine = b4 ? d[j + 4] : d[j], theirs = b4 ? d[j] : d[j + 4];
+      h4[j] = mine + __shfl_xor_sync(0xffffffffu, theirs, 16);
+    }
+#pragma unroll
+    for (int j = 0; j < 2; ++j) {
+      const float mine = b3 ? h4[j + 2] : h4[j], theirs = b3 ? h4[j] : h4[j + 2];
+      h2[j] = mine + __shfl_xor_sync(0xffffffffu, theirs, 8);
+    }
+    float raw;
+    {
+      const float mine = b2 ? h2[1] : h2[0], theirs = b2 ? h2[0] : h2[1];
+      raw = mine + __shfl_xor_sync(0xffffffffu, theirs, 4);
+    }
+    raw += __shfl_xor_sync(0xffffffffu, raw, 2);
+    raw += __shfl_xor_sync(0xffffffffu, raw, 1);
+    const int u = lane >> 2;  // this lane's key of the batch
+    if (i0 + u < n_keys) {
+      const float sc = cap_out > 0.f ? cap_out * tanhf(raw * cap_in) : raw * sl;
+      if ((lane & 3) == 0) s_sc[wid][i0 + u] = sc;
+      kmx = fmaxf(kmx, sc);
+    }
   }
+  mx = fmaxf(mx, warp_max(kmx));
   __syncwarp();
 
   // the splits' partials, then the tail keys in position order
@@ -1028,11 +1088,11 @@ __global__ void __launch_bounds__(128) attn_merge_tail_kernel(
   for (int e = 0; e < E; ++e) acc[e] = 0.f;
   float denom = 0.f;
   for (int sp = 0; sp < splits; ++sp) {
-    const size_t slot = (static_cast<size_t>(tile) * splits + sp) * kRows + r;
-    const float l = ws_ml[slot * 2 + 1];
+    const float* ml = part_ml(sp);
+    const float l = ml[1];
     if (!(l > 0.f)) continue;
-    const float w = exp2f(ws_ml[slot * 2] - mx);
-    const float* v = ws_o + slot * D + lane * E;
+    const float w = exp2f(ml[0] - mx);
+    const float* v = part_o(sp) + lane * E;
 #pragma unroll
     for (int e = 0; e < E; ++e) acc[e] += v[e] * w;
     denom += l * w;
@@ -1041,7 +1101,7 @@ __global__ void __launch_bounds__(128) attn_merge_tail_kernel(
     float vv[kTailBatch][E];
 #pragma unroll
     for (int u = 0; u < kTailBatch; ++u)
-      if (i0 + u < n_keys) load_kv<E>(v_cache, kv_row(pages, b, Hkv, kvh, S, s_row[wid][i0 + u]), lane, fp8, vv[u]);
+      if (i0 + u < n_keys) load_kv<E>(v_stage, s_row[wid][i0 + u], lane, fp8, vv[u]);
 #pragma unroll
     for (int u = 0; u < kTailBatch; ++u) {
       if (i0 + u < n_keys) {
@@ -1310,12 +1370,16 @@ int launch_attention(const void* q, const CUtensorMap* tm_k, const CUtensorMap* 
   float* ws_ml = staged ? ws + static_cast<size_t>(ctas) * plan.splits * kRows * D : nullptr;
   dim3 grid(ctas, plan.splits);
   const float sl2 = scale * 1.4426950408889634f;
+  cudaError_t launch_err = cudaSuccess;  // a refused launch (e.g. a shared-memory request) returns -3
+  auto note = [&](cudaError_t e) {
+    if (e != cudaSuccess && launch_err == cudaSuccess) launch_err = e;
+  };
   auto run = [&](auto kernel, int smem) {
-    set_max_smem(kernel, smem);
-    launch_pdl(kernel, grid, dim3(kThreads), smem, stream, static_cast<const bf16*>(q), *tm_k, *tm_v,
+    note(set_max_smem(kernel, smem));
+    note(launch_pdl(kernel, grid, dim3(kThreads), smem, stream, static_cast<const bf16*>(q), *tm_k, *tm_v,
                static_cast<bf16*>(out), ws_o, ws_ml, kv_len, n_new, mask, T, H, Hkv, S, sl2, q_offset,
                plan.chunks_per_split, plan.m_tiles, status, trace, k_scale, v_scale, keep, lse_out, kivi, kivi_chunks,
-               kivi_bits, tail_w, opts, pages);
+               kivi_bits, tail_w, opts, pages));
   };
   // bf16 caches without KIVI codes take the pipelined walk (ECZ_ATTN_PIPE=0 selects the serial one, for comparison)
   static const bool pipe_env = [] {
@@ -1339,18 +1403,20 @@ int launch_attention(const void* q, const CUtensorMap* tm_k, const CUtensorMap* 
   if (tail_w > 0) {
     auto merge = D == 64 ? attn_merge_tail_kernel<64> : D == 256 ? attn_merge_tail_kernel<256>
                                                                  : attn_merge_tail_kernel<128>;
-    launch_pdl(merge, mgrid, dim3(128), 0, stream, static_cast<const float*>(ws_o),
-               static_cast<const float*>(ws_ml), static_cast<bf16*>(out), T, H, Hkv, plan.m_tiles, plan.splits,
-               lse_out, static_cast<const bf16*>(q), static_cast<const uint8_t*>(k_cache),
-               static_cast<const uint8_t*>(v_cache), kv_len, n_new, mask, S, sl2, q_offset, tail_w, k_scale, v_scale,
-               keep, opts.softcap, opts.sinks, pages, status);
+    const int stage = tail_stage_bytes(D, fp8, tail_w);
+    if (stage > 48 * 1024) note(set_max_smem(merge, stage));
+    note(launch_pdl(merge, mgrid, dim3(128), stage, stream, static_cast<const float*>(ws_o),
+                    static_cast<const float*>(ws_ml), static_cast<bf16*>(out), T, H, Hkv, plan.m_tiles, plan.splits,
+                    lse_out, static_cast<const bf16*>(q), static_cast<const uint8_t*>(k_cache),
+                    static_cast<const uint8_t*>(v_cache), kv_len, n_new, mask, S, sl2, q_offset, tail_w, k_scale,
+                    v_scale, keep, opts.softcap, opts.sinks, pages, status));
   } else if (plan.splits > 1) {
     auto merge = D == 64 ? attn_merge_kernel<64> : D == 256 ? attn_merge_kernel<256> : attn_merge_kernel<128>;
-    launch_pdl(merge, mgrid, dim3(128), 0, stream, static_cast<const float*>(ws_o),
-               static_cast<const float*>(ws_ml), static_cast<bf16*>(out), T, H, Hkv, plan.m_tiles, plan.splits,
-               lse_out, opts.sinks);
+    note(launch_pdl(merge, mgrid, dim3(128), 0, stream, static_cast<const float*>(ws_o),
+                    static_cast<const float*>(ws_ml), static_cast<bf16*>(out), T, H, Hkv, plan.m_tiles,
+                    plan.splits, lse_out, opts.sinks));
   }
-  return 0;
+  return launch_err == cudaSuccess ? 0 : -3;
 }
 
 int launch_attention_scores(const void* q, const CUtensorMap* tm_k, const float* lse2, float* scores,

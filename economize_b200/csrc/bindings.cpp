@@ -409,6 +409,10 @@ Tensor attention(Tensor q, Tensor k_cache, Tensor v_cache, Tensor kv_len, Tensor
                                        kivi.has_value() ? kivi_chunks->data_ptr<int>() : nullptr,
                                        static_cast<int>(kivi_bits), static_cast<int>(tail), k_cache.data_ptr(),
                                        v_cache.data_ptr(), opts, ck.pages);
+  if (rc == -3) {
+    const cudaError_t err = cudaGetLastError();  // clears the refused launch's error state
+    TORCH_CHECK(false, "attention: a kernel launch was refused: ", cudaGetErrorString(err));
+  }
   TORCH_CHECK(rc == 0, "attention: unsupported shape (head_dim 64, 128 or 256, fp8 and KIVI caches at 128, H "
               "divisible by H_kv)");
   return out;

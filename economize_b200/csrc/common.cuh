@@ -12,8 +12,8 @@
 #include <cuda_runtime.h>
 #include <stdint.h>
 
+#include <map>
 #include <mutex>
-#include <set>
 #include <utility>
 
 #include "launchers.h"  // KVPages, KVLayout
@@ -293,18 +293,19 @@ __device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;"
 bool pdl_enabled();
 
 // Raise a kernel's dynamic shared-memory limit on the CURRENT device. The attribute belongs to the (kernel, device)
-// pair, so a process that launches on several GPUs must set it on each; this records which pairs are done (under a
-// lock, so host threads may launch concurrently) and sets each one once.
+// pair, so a process that launches on several GPUs must set it on each; this records the largest size set for each
+// pair (under a lock, so host threads may launch concurrently) and sets it again only for a larger request.
 inline cudaError_t set_max_smem(const void* kernel, int bytes) {
   static std::mutex mu;
-  static std::set<std::pair<const void*, int>> done;
+  static std::map<std::pair<const void*, int>, int> done;  // the largest size set per (kernel, device)
   int device = 0;
   cudaError_t err = cudaGetDevice(&device);
   if (err != cudaSuccess) return err;
   std::lock_guard<std::mutex> lock(mu);
-  if (done.count({kernel, device}) != 0) return cudaSuccess;
+  auto it = done.find({kernel, device});
+  if (it != done.end() && it->second >= bytes) return cudaSuccess;
   err = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
-  if (err == cudaSuccess) done.insert({kernel, device});
+  if (err == cudaSuccess) done[{kernel, device}] = bytes;
   return err;
 }
 
