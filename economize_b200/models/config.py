@@ -28,10 +28,11 @@ __all__ = ["ModelConfig", "SUPPORTED_MODEL_TYPES", "gpt_oss_20b", "llama31_8b", 
 #: separate rotary tables for the sliding-window layers (gemma3_text), per-layer sliding windows (mistral, ministral,
 #: gemma2, gemma3_text, olmo3, qwen2 with use_sliding_window), sparse MoE with q/k norms (olmoe) and a gated shared
 #: expert (qwen2_moe), and biased projections everywhere with attention sink logits, YaRN rotary scaling and
-#: clamped-SwiGLU experts (gpt_oss).
+#: clamped-SwiGLU experts (gpt_oss), Granite's scales around MoE blocks with an ungated shared expert (granitemoe,
+#: granitemoeshared), and YaRN with position-scaled queries (ministral3).
 SUPPORTED_MODEL_TYPES = ("llama", "mistral", "qwen2", "qwen3", "mixtral", "granite", "phi3", "smollm3", "olmo2",
                          "qwen3_moe", "gemma", "gemma2", "gemma3_text", "ministral", "olmo3", "olmoe", "qwen2_moe",
-                         "gpt_oss", "economize_b200")
+                         "gpt_oss", "granitemoe", "granitemoeshared", "ministral3", "economize_b200")
 
 #: the layer kinds of ``ModelConfig.layer_types``
 FULL, SLIDING = "full_attention", "sliding_attention"
@@ -89,8 +90,13 @@ class ModelConfig:
     #: rotary parameters of the sliding-window layers when they differ from the others' (Gemma-3: {"rope_theta":
     #: 1e4}; keys as ``rope_scaling`` plus ``rope_theta``)
     local_rope: dict[str, Any] | None = None
-    #: width of a shared expert added to every sparse MoE MLP, gated by sigmoid(x . w) (Qwen2-MoE; 0: none)
+    #: width of a shared expert added to every sparse MoE MLP, gated by sigmoid(x . w) (Qwen2-MoE) or added as it
+    #: is (``shared_expert_gated=False``, GraniteMoE-shared); 0: none
     shared_expert_size: int = 0
+    shared_expert_gated: bool = True
+    #: queries scaled by 1 + beta ln(1 + floor(position / original)) after the rotary embedding (Ministral-3's
+    #: ``llama_4_scaling_beta``): (beta, original), or None
+    query_position_scale: tuple[float, float] | None = None
     #: gpt-oss: a bias on the attention output projection, one learned sink logit per query head that joins every
     #: softmax denominator, and biases on the router and on both expert projections
     o_bias: bool = False
@@ -102,6 +108,9 @@ class ModelConfig:
         if self.head_dim is None:
             self.head_dim = self.hidden_size // self.num_heads
         self.nope_layers = tuple(int(i) for i in self.nope_layers)
+        if self.query_position_scale is not None:
+            beta, original = self.query_position_scale
+            self.query_position_scale = (float(beta), float(original))
         self.layer_types = tuple(str(t) for t in self.layer_types)
         if self.num_heads % self.num_kv_heads:
             raise UnsupportedModelError(f"{self.num_heads} heads do not split into {self.num_kv_heads} KV groups")
@@ -137,7 +146,7 @@ class ModelConfig:
         h, f, layers = self.hidden_size, self.intermediate_size, self.num_layers
         attn = h * (self.q_size + 2 * self.kv_size) + self.q_size * h
         mlp = 3 * h * f * (self.num_experts if self.is_moe else 1) + (h * self.num_experts if self.is_moe else 0)
-        mlp += 3 * h * self.shared_expert_size + (h if self.shared_expert_size else 0)
+        mlp += 3 * h * self.shared_expert_size + (h if self.shared_expert_size and self.shared_expert_gated else 0)
         if self.moe_bias:
             mlp += self.num_experts * (2 * f + h + 1)
         attn += (h if self.o_bias else 0) + (self.num_heads if self.attn_sinks else 0)
@@ -175,7 +184,7 @@ class ModelConfig:
         kinds = list(get("layer_types", None) or [])
         if model_type == "qwen2" and not get("use_sliding_window", False):
             kinds, window = [], 0
-        if not kinds and window and model_type in ("mistral", "ministral"):
+        if not kinds and window and model_type in ("mistral", "ministral", "ministral3"):
             kinds = [SLIDING] * layers
         if kinds and SLIDING in kinds:
             extra.update(layer_types=tuple(kinds), sliding_window=window)
@@ -216,7 +225,7 @@ class ModelConfig:
         if model_type == "smollm3":
             flags = list(get("no_rope_layers", []) or [])
             extra["nope_layers"] = tuple(i for i, use_rope in enumerate(flags) if not use_rope)
-        if model_type == "granite":
+        if model_type in ("granite", "granitemoe", "granitemoeshared"):
             extra.update(embedding_multiplier=float(get("embedding_multiplier", 1.0)),
                          residual_multiplier=float(get("residual_multiplier", 1.0)),
                          attention_multiplier=float(get("attention_multiplier", 1.0)),
@@ -227,6 +236,11 @@ class ModelConfig:
             if get("clip_qkv"):
                 raise UnsupportedModelError("olmoe with clip_qkv is not supported")
             extra.update(qk_norm_full=True)
+        if model_type == "granitemoeshared":
+            extra.update(shared_expert_size=int(get("shared_intermediate_size", 0) or 0), shared_expert_gated=False)
+        if model_type == "ministral3" and isinstance(rope, dict) and rope.get("llama_4_scaling_beta"):
+            extra["query_position_scale"] = (float(rope["llama_4_scaling_beta"]),
+                                             float(rope["original_max_position_embeddings"]))
         if model_type == "qwen2_moe":
             if int(get("decoder_sparse_step", 1) or 1) != 1 or list(get("mlp_only_layers", []) or []):
                 raise UnsupportedModelError("qwen2_moe with dense layers between the sparse ones is not supported")
@@ -285,6 +299,24 @@ class ModelConfig:
             return transformers.Gemma3TextConfig(rope_parameters={FULL: full, SLIDING: local},
                                                  attn_logit_softcapping=self.attn_softcap,
                                                  final_logit_softcapping=self.final_softcap, **gem)
+        if kind in ("granitemoe", "granitemoeshared"):
+            scales = dict(embedding_multiplier=self.embedding_multiplier, residual_multiplier=self.residual_multiplier,
+                          attention_multiplier=self.attention_multiplier or self.head_dim ** -0.5,
+                          logits_scaling=self.logits_scaling, num_local_experts=self.num_experts,
+                          num_experts_per_tok=self.experts_per_token)
+            rest = {k: v for k, v in common.items() if k != "head_dim"}
+            if kind == "granitemoe":
+                return transformers.GraniteMoeConfig(**scales, **rest)
+            return transformers.GraniteMoeSharedConfig(shared_intermediate_size=self.shared_expert_size, **scales,
+                                                       **rest)
+        if kind == "ministral3":
+            rope = {"rope_type": "default", "rope_theta": self.rope_theta, **(self.rope_scaling or {})}
+            if self.query_position_scale is not None:
+                rope.update(llama_4_scaling_beta=self.query_position_scale[0],
+                            original_max_position_embeddings=int(self.query_position_scale[1]))
+            rest = {k: v for k, v in common.items() if k not in ("rope_theta", "rope_scaling", "attention_bias")}
+            return transformers.Ministral3Config(rope_parameters=rope, sliding_window=self.sliding_window or None,
+                                                 **rest)
         if kind == "gpt_oss":
             rope = {"rope_type": "default", "rope_theta": self.rope_theta, **(self.rope_scaling or {})}
             gpt = {k: v for k, v in common.items() if k not in ("rope_theta", "rope_scaling", "attention_bias")}

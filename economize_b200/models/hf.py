@@ -71,6 +71,14 @@ def load_hf_state(model, state: dict[str, torch.Tensor]) -> None:
             layer.b_gate_up.copy_(torch.cat([b[:, 0::2], b[:, 1::2]], 1))
             layer.w_down.copy_(_take(state, x + "down_proj").transpose(1, 2))
             layer.b_down.copy_(_take(state, x + "down_proj_bias"))
+        elif c.is_moe and c.model_type in ("granitemoe", "granitemoeshared"):
+            m = p + "block_sparse_moe."
+            layer.router.copy_(_take(state, m + "router.layer.weight"))
+            layer.w_gate_up.copy_(_take(state, m + "input_linear.weight"))  # [E, 2F, H], gate half first
+            layer.w_down.copy_(_take(state, m + "output_linear.weight"))
+            if layer.w_shared_gate_up is not None:
+                layer.w_shared_gate_up.copy_(_take(state, p + "shared_mlp.input_linear.weight"))
+                layer.w_shared_down.copy_(_take(state, p + "shared_mlp.output_linear.weight"))
         elif c.is_moe:
             if p + "mlp.experts.gate_up_proj" in state:
                 layer.router.copy_(_take(state, p + "mlp.gate.weight"))
@@ -157,6 +165,14 @@ def export_hf_state(model, copy: bool = True) -> dict[str, torch.Tensor]:
             out[x + "gate_up_proj_bias"] = torch.stack([bg, bu], 2).reshape(bg.shape[0], -1)
             out[x + "down_proj"] = full(layer.w_down).transpose(1, 2)
             out[x + "down_proj_bias"] = layer.b_down.detach()
+        elif c.is_moe and c.model_type in ("granitemoe", "granitemoeshared"):
+            m = p + "block_sparse_moe."
+            out[m + "router.layer.weight"] = layer.router.detach()
+            out[m + "input_linear.weight"] = full(layer.w_gate_up)
+            out[m + "output_linear.weight"] = full(layer.w_down)
+            if layer.w_shared_gate_up is not None:
+                out[p + "shared_mlp.input_linear.weight"] = full(layer.w_shared_gate_up)
+                out[p + "shared_mlp.output_linear.weight"] = full(layer.w_shared_down)
         elif c.is_moe:
             out[p + "mlp.gate.weight"] = layer.router.detach()
             out[p + "mlp.experts.gate_up_proj"] = full(layer.w_gate_up)

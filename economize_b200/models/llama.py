@@ -56,7 +56,7 @@ class DecoderLayer(nn.Module):
         se = config.shared_expert_size if config.is_moe else 0
         self.w_shared_gate_up = nn.Parameter(torch.empty(2 * se, h, **kw)) if se else None
         self.w_shared_down = nn.Parameter(torch.empty(h, se, **kw)) if se else None
-        self.shared_gate = nn.Parameter(torch.empty(1, h, **kw)) if se else None
+        self.shared_gate = nn.Parameter(torch.empty(1, h, **kw)) if se and config.shared_expert_gated else None
         #: attention sink logits of this layer's query heads (fp32 [H]; gpt-oss), or None
         self.sinks = nn.Parameter(torch.zeros(config.num_heads, dtype=torch.float32, device=device)) \
             if config.attn_sinks else None
@@ -467,6 +467,10 @@ class CausalLM(nn.Module):
                            c.head_dim, k_cache,
                            v_cache, batch.kv_len, batch.n_new, q_norm, k_norm, c.rms_norm_eps,
                            q_offset=batch.q_offset, k_scale=k_scale, v_scale=v_scale, pages=pages)
+        if c.query_position_scale is not None:  # Ministral-3: 1 + beta ln(1 + floor(p / original)), in q's dtype
+            beta, original = c.query_position_scale
+            pos = batch.positions.to(torch.float32)
+            q = q * (1.0 + beta * torch.log1p(torch.floor(pos / original))).to(q.dtype)[..., None, None]
         keep = self.kv_evictor.keep_for(index, k_cache, q, batch) if self.kv_evictor is not None else None
         sparse = self.prefill_sparsity
         if sparse is not None and sparse.active:  # sparse prefill (MInference): keys the chunk's pattern hides
@@ -511,10 +515,11 @@ class CausalLM(nn.Module):
             out = moe_mlp(x, layer.router, layer.w_gate_up, layer.w_down, c.experts_per_token,
                           getattr(self, "ep", None), renormalize=c.norm_topk_prob, act=c.hidden_act,
                           limit=c.swiglu_limit, biases=biases)
-            if layer.w_shared_gate_up is not None:  # Qwen2-MoE's gated shared expert
+            if layer.w_shared_gate_up is not None:  # a shared expert: Qwen2-MoE gates it, GraniteMoE-shared not
                 shared = ops.linear(ops.silu_mul(ops.linear(x, layer.w_shared_gate_up)), layer.w_shared_down)
-                gate = torch.sigmoid(ops.linear(x, self._gate_rows(layer))[..., :1])
-                out = out + gate * shared
+                if layer.shared_gate is not None:
+                    shared = torch.sigmoid(ops.linear(x, self._gate_rows(layer))[..., :1]) * shared
+                out = out + shared
             return out
         if self.observer is not None:
             self.observer(index, "w_gate_up", x)

@@ -200,7 +200,7 @@ def _check_plain_block(config) -> None:
                 "soft-caps": bool(config.attn_softcap), "sink logits": config.attn_sinks,
                 "an output-projection bias": config.o_bias, "a non-SwiGLU activation": config.hidden_act != "silu",
                 "scaled attention or residuals": config.attention_multiplier is not None
-                or config.residual_multiplier != 1.0}
+                or config.residual_multiplier != 1.0, "position-scaled queries": config.query_position_scale is not None}
     found = [name for name, present in variants.items() if present]
     if found:
         raise ConfigError(f"the PyTorch training block models the Llama block; {config.model_type} has "

@@ -37,6 +37,17 @@ FAMILIES = {
     "olmoe": dict(num_experts=4, num_experts_per_tok=2, norm_topk_prob=False),
     "qwen2_moe": dict(num_experts=4, num_experts_per_tok=2, moe_intermediate_size=48,
                       shared_expert_intermediate_size=40, norm_topk_prob=False),
+    # Granite's scales around MoE blocks; the shared variant adds an ungated shared expert
+    "granitemoe": dict(num_local_experts=4, num_experts_per_tok=2, embedding_multiplier=6.0, residual_multiplier=0.3,
+                       attention_multiplier=0.02, logits_scaling=4.0),
+    "granitemoeshared": dict(num_local_experts=4, num_experts_per_tok=2, shared_intermediate_size=40,
+                             embedding_multiplier=6.0, residual_multiplier=0.3, attention_multiplier=0.02,
+                             logits_scaling=4.0),
+    # YaRN and queries scaled by position beyond the original context (small here, so the scale moves)
+    "ministral3": dict(head_dim=16, eos_token_id=None, rope_parameters={"rope_type": "yarn", "rope_theta": 10000.0, "factor": 4.0,
+                                                     "original_max_position_embeddings": 8, "beta_fast": 32.0,
+                                                     "beta_slow": 1.0, "mscale": 1.0, "mscale_all_dim": 1.0,
+                                                     "llama_4_scaling_beta": 0.1}),
     # biased q/k/v/o, sink logits, sliding windows on alternate layers, YaRN, clamped-SwiGLU experts with biases
     "gpt_oss": dict(head_dim=16, num_local_experts=4, num_experts_per_tok=2, sliding_window=6,
                     rope_parameters={"rope_type": "yarn", "factor": 4.0, "beta_fast": 32.0, "beta_slow": 1.0,

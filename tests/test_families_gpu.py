@@ -34,6 +34,16 @@ FAMILIES = {
     "olmoe": dict(num_experts=8, num_experts_per_tok=2, norm_topk_prob=False, intermediate_size=256),
     "qwen2_moe": dict(num_experts=8, num_experts_per_tok=2, moe_intermediate_size=256,
                       shared_expert_intermediate_size=384, norm_topk_prob=False),
+    "granitemoe": dict(num_local_experts=8, num_experts_per_tok=2, intermediate_size=256, embedding_multiplier=6.0,
+                       residual_multiplier=0.3, attention_multiplier=0.0125, logits_scaling=4.0),
+    "granitemoeshared": dict(num_local_experts=8, num_experts_per_tok=2, intermediate_size=256,
+                             shared_intermediate_size=384, embedding_multiplier=6.0, residual_multiplier=0.3,
+                             attention_multiplier=0.0125, logits_scaling=4.0),
+    # YaRN; queries scaled by position past 64 tokens
+    "ministral3": dict(head_dim=64, eos_token_id=None,
+                       rope_parameters={"rope_type": "yarn", "rope_theta": 1e6, "factor": 4.0,
+                                        "original_max_position_embeddings": 64, "beta_fast": 32.0, "beta_slow": 1.0,
+                                        "mscale": 1.0, "mscale_all_dim": 1.0, "llama_4_scaling_beta": 0.1}),
     # biased projections, sink logits, sliding windows on alternate layers, YaRN, clamped-SwiGLU biased experts
     "gpt_oss": dict(head_dim=64, num_local_experts=8, num_experts_per_tok=4, intermediate_size=256,
                     sliding_window=80),
