@@ -1313,6 +1313,39 @@ Tensor sp_linear_ag(std::vector<int64_t> ptrs, int64_t rank, int64_t hidden, int
   return y;
 }
 
+// All-gather -> GEMM on the swap-AB kernel for a consumer that fuses the split-K reduction (rope_store, the gated
+// activation): the split-K partials [splits, rows, N] (fp32), or [rows, N] bf16 when K is not split, as linear_parts.
+Tensor sp_linear_ag_parts(std::vector<int64_t> ptrs, int64_t rank, int64_t hidden, int64_t max_rows, int64_t n_cap,
+                          int64_t rows, Tensor w) {
+  CHECK_CUDA(w);
+  CHECK_BF16(w);
+  const ecz::SpLayout L = sp_check(ptrs, rank, hidden, max_rows, n_cap);
+  TORCH_CHECK(w.dim() == 2 && w.size(1) == hidden && rows >= 1 && rows <= max_rows, "sp_linear_ag_parts: w [N, H]");
+  const int M = static_cast<int>(rows), K = static_cast<int>(hidden), N = static_cast<int>(w.size(0));
+  const int bn = ecz::gemm_block_n(M);
+  TORCH_CHECK(bn <= 64, "sp_linear_ag_parts serves passes of at most 64 rows");
+  c10::cuda::CUDAGuard guard(w.device());
+  w = w.contiguous();
+  const int sms = num_sms(w.get_device());
+  int splits = std::min(8, ecz::gemm_splits(M, N, K, 2 * sms));
+  const int total_kb = (K + 63) / 64, kbps = (total_kb + splits - 1) / splits;
+  splits = (total_kb + kbps - 1) / kbps;  // the launcher drops empty splits the same way
+  const char* ag = reinterpret_cast<const char*>(ptrs[rank]) + L.ag_off;
+  const CUtensorMap* tw = tensor_map(w.data_ptr(), N, K, K, 128);
+  const CUtensorMap* tx0 = tensor_map(ag, M, K, K, bn);
+  const CUtensorMap* tx1 = tensor_map(ag + static_cast<size_t>(max_rows) * hidden * 2, M, K, K, bn);
+  ecz::AgWait wait;
+  wait.ctrl = reinterpret_cast<unsigned*>(ptrs[rank]);
+  wait.world = static_cast<int>(ptrs.size());
+  Tensor out = splits > 1 ? at::empty({splits, M, N}, w.options().dtype(at::kFloat)) : at::empty({M, N}, w.options());
+  const int rc = ecz::launch_gemm_bf16(tw, tx0, splits > 1 ? nullptr : out.data_ptr(),
+                                       splits > 1 ? out.data_ptr<float>() : nullptr, M, N, K, splits,
+                                       status_word(w.device()), at::cuda::getCurrentCUDAStream(), nullptr, nullptr,
+                                       3, &wait, tx1);
+  TORCH_CHECK(rc == 0, "sp_linear_ag_parts: launch failed (", rc, ")");
+  return out;
+}
+
 // GEMM -> reduce-scatter: x [rows, K] . w^T with every output row stored into its owner rank's partial slot.
 void sp_linear_rs(std::vector<int64_t> ptrs, int64_t rank, int64_t hidden, int64_t max_rows, int64_t n_cap,
                   Tensor x, Tensor w) {
@@ -1496,6 +1529,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("sp_reduce_norm", &sp_reduce_norm, "reduce-scatter partials + residual + RMSNorm, all-gather the rows");
   m.def("sp_fetch", &sp_fetch, "wait for the current all-gather round and copy its rows");
   m.def("sp_capture", &sp_capture, "copy the captured residual rows of a capture slot");
+  m.def("sp_linear_ag_parts", &sp_linear_ag_parts, "all-gather -> split-K GEMM whose partials a fused consumer sums");
   m.def("sp_linear_ag", &sp_linear_ag, "all-gather -> GEMM (the GEMM waits for every rank's rows)");
   m.def("sp_linear_rs", &sp_linear_rs, "GEMM -> reduce-scatter (rows stored into their owner's partial slot)");
   m.def("reduce_rmsnorm", &reduce_rmsnorm, "wait for every rank's partial, sum, add residual, RMSNorm");

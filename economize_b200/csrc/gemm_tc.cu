@@ -112,7 +112,8 @@ template <int BN, int OCC = 1>
 __global__ void __launch_bounds__(128, OCC)
     gemm_swapab_kernel(const __grid_constant__ CUtensorMap tm_w, const __grid_constant__ CUtensorMap tm_x,
                        bf16* __restrict__ y, float* __restrict__ ws, int* __restrict__ counters, int M, int N,
-                       int K, int kb_per_split, unsigned* status, PeerOut peer) {
+                       int K, int kb_per_split, unsigned* status, PeerOut peer, AgWait ag,
+                       const __grid_constant__ CUtensorMap tm_x1) {
   using Cfg = GemmCfg<BN, OCC>;
   constexpr int S = Cfg::kStages;
   extern __shared__ uint8_t smem_raw[];
@@ -150,17 +151,21 @@ __global__ void __launch_bounds__(128, OCC)
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
 
+  int ag_par = 0;
   if (nkb > 0 && warp == 0 && lane == 0) {
     // ---- TMA producer ----
     // The weights do not depend on the previous kernel: the first ring of weight tiles is requested before
-    // griddepcontrol.wait, so it streams while the predecessor finishes; activations follow after the wait.
+    // griddepcontrol.wait, so it streams while the predecessor finishes; activations follow after the wait (and,
+    // for an all-gather -> GEMM, after every rank's rows arrived in this round's half of the buffer).
     const int pre = nkb < S ? nkb : S;
     for (int kb = 0; kb < pre; ++kb) {
       mbar_arrive_expect_tx(&full[kb], Cfg::kStageBytes);
       tma_load_2d(a_tiles + kb * kABytes, &tm_w, &full[kb], (kb0 + kb) * kBK, n0);
     }
     pdl_wait();
-    for (int kb = 0; kb < pre; ++kb) tma_load_2d(b_tiles + kb * Cfg::kBBytes, &tm_x, &full[kb], (kb0 + kb) * kBK, m0);
+    if (ag.ctrl != nullptr) ag_par = ag_wait(ag, status);
+    const CUtensorMap* mx = ag_par ? &tm_x1 : &tm_x;
+    for (int kb = 0; kb < pre; ++kb) tma_load_2d(b_tiles + kb * Cfg::kBBytes, mx, &full[kb], (kb0 + kb) * kBK, m0);
     for (int kb = pre; kb < nkb; ++kb) {
       const int s = kb % S;
       const uint32_t use = kb / S;
@@ -168,7 +173,7 @@ __global__ void __launch_bounds__(128, OCC)
       mbar_arrive_expect_tx(&full[s], Cfg::kStageBytes);
       const int kx = (kb0 + kb) * kBK;
       tma_load_2d(a_tiles + s * kABytes, &tm_w, &full[s], kx, n0);
-      tma_load_2d(b_tiles + s * Cfg::kBBytes, &tm_x, &full[s], kx, m0);
+      tma_load_2d(b_tiles + s * Cfg::kBBytes, mx, &full[s], kx, m0);
     }
   } else if (nkb > 0 && warp == 1 && lane == 0) {
     // ---- MMA issuer ----
@@ -292,6 +297,10 @@ __global__ void __launch_bounds__(128, OCC)
     wrote = last;
   }
   if (peer.world > 0 && ok) push_signal(peer, wrote, gridDim.x * gridDim.y, peer.parity);
+  if (ag.ctrl != nullptr && threadIdx.x == 0) {  // the last CTA closes the all-gather round (see ag_release)
+    const int par = nkb > 0 ? ag_par : static_cast<int>(ag.ctrl[kSpAgRound] & 1u);
+    ag_release(ag, par, gridDim.x * gridDim.y * gridDim.z);
+  }
 }
 
 __global__ void __launch_bounds__(256) splitk_reduce_kernel(const float* __restrict__ ws, bf16* __restrict__ y,
@@ -317,7 +326,9 @@ __global__ void __launch_bounds__(256) splitk_reduce_kernel(const float* __restr
 // flags: bit 0 = two CTAs per SM for skinny tiles, bit 1 = leave the fp32 partials in ws (no reduction)
 template <int BN>
 int run_gemm(const CUtensorMap& tm_w, const CUtensorMap& tm_x, void* y, float* ws, int* counters, int M, int N,
-             int K, int splits, unsigned* status, cudaStream_t stream, const PeerOut& peer, int flags = 0) {
+             int K, int splits, unsigned* status, cudaStream_t stream, const PeerOut& peer, int flags = 0,
+             const AgWait& ag = AgWait{}, const CUtensorMap* tm_x1 = nullptr) {
+  const CUtensorMap& x1 = tm_x1 != nullptr ? *tm_x1 : tm_x;
   constexpr int kOcc2 = split_occupancy<BN>();
   const bool occ2 = (flags & 1) != 0 && kOcc2 == 2;
   set_max_smem(gemm_swapab_kernel<BN, 1>, GemmCfg<BN, 1>::kSmem);
@@ -329,11 +340,11 @@ int run_gemm(const CUtensorMap& tm_w, const CUtensorMap& tm_x, void* y, float* w
   if (occ2) {
     launch_pdl(gemm_swapab_kernel<BN, kOcc2>, grid, dim3(128), GemmCfg<BN, kOcc2>::kSmem, stream, tm_w, tm_x,
                static_cast<bf16*>(y), splits > 1 ? ws : nullptr, splits > 1 ? counters : nullptr, M, N, K, kbps,
-               status, peer);
+               status, peer, ag, x1);
   } else {
     launch_pdl(gemm_swapab_kernel<BN, 1>, grid, dim3(128), GemmCfg<BN, 1>::kSmem, stream, tm_w, tm_x,
                static_cast<bf16*>(y), splits > 1 ? ws : nullptr, splits > 1 ? counters : nullptr, M, N, K, kbps,
-               status, peer);
+               status, peer, ag, x1);
   }
   if (splits > 1 && counters == nullptr && (flags & 2) == 0) {
     const long total = static_cast<long>(M) * N;
@@ -911,16 +922,20 @@ int launch_gemm_persistent(const CUtensorMap* tm_w, const CUtensorMap* tm_x, voi
 
 int launch_gemm_bf16(const CUtensorMap* tm_w, const CUtensorMap* tm_x, void* y, float* ws, int M, int N, int K,
                      int splits, unsigned* status, cudaStream_t stream, int* counters, const PeerOut* peer,
-                     int flags) {
+                     int flags, const AgWait* ag, const CUtensorMap* tm_x1) {
   if (K % 8 != 0 || N % 4 != 0) return -1;
   if (splits > 1 && counters == nullptr && peer != nullptr && peer->world > 0) return -1;  // push needs the fused reduce
   const PeerOut none{};
   const PeerOut& pe = peer != nullptr ? *peer : none;
+  const AgWait none_ag{};
+  const AgWait& aw = ag != nullptr ? *ag : none_ag;
   switch (gemm_block_n(M)) {
-    case 32: return run_gemm<32>(*tm_w, *tm_x, y, ws, counters, M, N, K, splits, status, stream, pe, flags);
-    case 64: return run_gemm<64>(*tm_w, *tm_x, y, ws, counters, M, N, K, splits, status, stream, pe, flags);
-    case 128: return run_gemm<128>(*tm_w, *tm_x, y, ws, counters, M, N, K, splits, status, stream, pe, flags);
-    default: return run_gemm<256>(*tm_w, *tm_x, y, ws, counters, M, N, K, splits, status, stream, pe, flags);
+    case 32: return run_gemm<32>(*tm_w, *tm_x, y, ws, counters, M, N, K, splits, status, stream, pe, flags, aw, tm_x1);
+    case 64: return run_gemm<64>(*tm_w, *tm_x, y, ws, counters, M, N, K, splits, status, stream, pe, flags, aw, tm_x1);
+    case 128:
+      return run_gemm<128>(*tm_w, *tm_x, y, ws, counters, M, N, K, splits, status, stream, pe, flags, aw, tm_x1);
+    default:
+      return run_gemm<256>(*tm_w, *tm_x, y, ws, counters, M, N, K, splits, status, stream, pe, flags, aw, tm_x1);
   }
 }
 

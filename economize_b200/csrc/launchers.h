@@ -114,7 +114,8 @@ int gemm_splits(int M, int N, int K, int num_sms);
 // reduced inside the GEMM by the last CTA of each tile; without, by a second kernel.
 int launch_gemm_bf16(const CUtensorMap* tm_w, const CUtensorMap* tm_x, void* y, float* ws, int M, int N, int K,
                      int splits, unsigned* status, cudaStream_t stream, int* counters = nullptr,
-                     const PeerOut* peer = nullptr, int flags = 0);
+                     const PeerOut* peer = nullptr, int flags = 0, const AgWait* ag = nullptr,
+                     const CUtensorMap* tm_x1 = nullptr);
 
 // Cluster split-K GEMM (partials reduced over DSMEM inside each tile's cluster; no workspace).
 int gemm_cluster_splits(int M, int N, int K, int num_sms);

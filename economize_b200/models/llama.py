@@ -354,7 +354,7 @@ class CausalLM(nn.Module):
         c = self.config
         if c.is_moe or self.observer is not None or self.depth_policy is not None or c.post_norm or \
                 c.qk_norm_full or c.residual_multiplier != 1.0 or c.sandwich_norm or c.hidden_act != "silu" or \
-                c.final_softcap:
+                c.final_softcap or c.o_bias:
             return False
         return not any(getattr(layer, name, None) for layer in self.layers
                        for name in ("skip_attn", "skip_mlp", "mlp_rule", "attn_input_hook"))
@@ -377,13 +377,14 @@ class CausalLM(nn.Module):
         slot_of = {layer: slot for slot, layer in enumerate(wanted)}
         resid = sp.reduce_norm(resid, self.layers[0].attn_norm, eps, M, partials=False)
         for i, layer in enumerate(self.layers):
-            qkv = sp.ag_linear(layer.wqkv, M)
             if layer.bqkv is not None:
-                qkv = qkv + layer.bqkv
-            o = self._attend(layer, i, qkv.reshape(B, T, -1), batch, cache, cos, sin)
+                qkv = (sp.ag_linear(layer.wqkv, M) + layer.bqkv).reshape(B, T, -1)
+            else:  # split-K partials go straight into the rope / KV-store kernel
+                qkv = sp.ag_linear_parts(layer.wqkv, M, (B, T))
+            o = self._attend(layer, i, qkv, batch, cache, cos, sin)
             sp.rs_linear(o, layer.wo)
             resid = sp.reduce_norm(resid, layer.mlp_norm, eps, M)
-            a = ops.silu_mul(sp.ag_linear(layer.w_gate_up, M))
+            a = ops.silu_mul(sp.ag_linear_parts(layer.w_gate_up, M, (M,)))
             sp.rs_linear(a, layer.w_down)
             nxt = self.layers[i + 1].attn_norm if i + 1 < len(self.layers) else self.norm
             resid = sp.reduce_norm(resid, nxt, eps, M, capture=slot_of.get(i + 1, -1))

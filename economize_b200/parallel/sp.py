@@ -75,6 +75,17 @@ class SequenceParallel:
         """All-gather -> GEMM: ``X @ weight.T`` for the current all-gather round's ``[rows, H]`` activations."""
         return self.ext.sp_linear_ag(*self._args(), rows, weight)
 
+    def ag_linear_parts(self, weight: torch.Tensor, rows: int, lead: tuple[int, ...]) -> torch.Tensor | ops.Partials:
+        """:meth:`ag_linear` for a consumer that sums split-K partials (``ops.rope_store``, ``ops.glu``): the
+        swap-AB GEMM's :class:`~economize_b200.ops.Partials` shaped ``[*lead, N]`` (the decode path's kernel;
+        passes of more than 64 tokens take :meth:`ag_linear`)."""
+        if rows > 64:
+            return self.ag_linear(weight, rows).reshape(*lead, -1)
+        y = self.ext.sp_linear_ag_parts(*self._args(), rows, weight)
+        if y.dtype == torch.bfloat16:
+            return y.reshape(*lead, -1)
+        return ops.Partials(y.reshape(y.shape[0], *lead, y.shape[-1]))
+
     def rs_linear(self, x: torch.Tensor, weight: torch.Tensor) -> None:
         """GEMM -> reduce-scatter: ``x @ weight.T`` with every output row sent to its owner's partial slot."""
         self.ext.sp_linear_rs(*self._args(), x.reshape(-1, x.shape[-1]), weight)

@@ -73,6 +73,9 @@ class GlooSequenceParallel:
 
         return ops.linear(self.rows[:rows], w)
 
+    def ag_linear_parts(self, w, rows, lead):
+        return self.ag_linear(w, rows).reshape(*lead, -1)
+
     def fetch(self, rows, like):
         self.passes += 1
         return self.rows[:rows].clone()
