@@ -28,6 +28,7 @@ from .core.serialization import (FORMATS, Checkpoint, CheckpointFormat, attach, 
                                  read_checkpoint, save, teacher_fingerprint)
 from .decoding import DecodeConfig, DecodeResult, GreedySelector, SpecEngine, TokenSelector, TopPSampler
 from . import ops  # noqa: F401
+from . import compat  # noqa: F401  (registers the tskip checkpoint formats)
 from .errors import (CalibrationMismatchWarning, CheckpointFormatError, CommTimeoutError, ConfigError,
                      DuplicateNameError, EconomizeError, IncompatibleTechniquesError, KernelUnavailableError,
                      NonFiniteLossError, SimulatedPathWarning, TeacherMismatchWarning, UnknownFieldWarning,
