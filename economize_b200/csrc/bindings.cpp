@@ -438,6 +438,49 @@ Tensor glu_act(Tensor gu, int64_t act, double limit) {
 
 Tensor silu_mul(Tensor gu) { return glu_act(gu, 0, 0.0); }
 
+// Block Walsh-Hadamard transform of the last dimension of a bf16 tensor (blocks of `block`, a power of two in
+// [8, 8192] dividing the width), scaled by 1 / sqrt(block)
+Tensor hadamard(Tensor x, int64_t block) {
+  CHECK_CUDA(x);
+  TORCH_CHECK(x.scalar_type() == at::kBFloat16, "hadamard: bf16 input");
+  c10::cuda::CUDAGuard guard(x.device());
+  x = x.contiguous();
+  const int F = static_cast<int>(x.size(-1));
+  const int rows = F ? static_cast<int>(x.numel() / F) : 0;
+  auto out = at::empty_like(x);
+  if (rows == 0) return out;
+  const int rc = ecz::launch_hadamard(x.data_ptr(), out.data_ptr(), rows, F, static_cast<int>(block),
+                                      at::cuda::getCurrentCUDAStream());
+  TORCH_CHECK(rc != -3, "hadamard: the kernel launch was refused: ", cudaGetErrorString(cudaGetLastError()));
+  TORCH_CHECK(rc == 0, "hadamard: block ", block, " must be a power of two in [8, 8192] dividing the width ", F);
+  return out;
+}
+
+// act(gate) * up of a fused [gate; up] projection (bf16, or split-K partials), rotated by the block Hadamard
+// transform in the same kernel
+Tensor glu_hadamard(Tensor gu, int64_t act, double limit, int64_t block) {
+  CHECK_CUDA(gu);
+  c10::cuda::CUDAGuard guard(gu.device());
+  gu = gu.contiguous();
+  auto [splits, shape] = parts_of(gu);
+  const int F2 = static_cast<int>(shape.back());
+  int64_t numel = 1;
+  for (auto d : shape) numel *= d;
+  const int rows = F2 ? static_cast<int>(numel / F2) : 0;
+  shape.back() = F2 / 2;
+  auto out = at::empty(shape, gu.options().dtype(at::kBFloat16));
+  if (rows == 0) return out;
+  TORCH_CHECK(splits || gu.scalar_type() == at::kBFloat16, "glu_hadamard: bf16 input or fp32 split-K partials");
+  TORCH_CHECK(act >= 0 && act <= 2, "glu_hadamard: act 0 (SiLU), 1 (GELU tanh) or 2 (clamped SwiGLU)");
+  const int rc = ecz::launch_hadamard(splits ? nullptr : gu.data_ptr(), out.data_ptr(), rows, F2 / 2,
+                                      static_cast<int>(block), at::cuda::getCurrentCUDAStream(), static_cast<int>(act),
+                                      splits ? gu.data_ptr<float>() : nullptr, splits, static_cast<float>(limit));
+  TORCH_CHECK(rc != -3, "glu_hadamard: the kernel launch was refused: ", cudaGetErrorString(cudaGetLastError()));
+  TORCH_CHECK(rc == 0, "glu_hadamard: block ", block, " must be a power of two in [8, 8192] dividing the width ",
+              F2 / 2);
+  return out;
+}
+
 Tensor linear_bf16(Tensor x, Tensor w) {
   CHECK_CUDA(x);
   CHECK_BF16(x);
@@ -1479,6 +1522,8 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
         py::arg("k_cache"), py::arg("kv_len"), py::arg("n_new"), py::arg("mask"), py::arg("lse2"), py::arg("scores"),
         py::arg("scale"), py::arg("q_offset"), py::arg("pages") = py::none());
   m.def("silu_mul", &silu_mul, "SwiGLU activation of [gate; up]");
+  m.def("hadamard", &hadamard, "block Walsh-Hadamard transform of the last dimension (QuaRot online rotation)");
+  m.def("glu_hadamard", &glu_hadamard, "act(gate) * up of [gate; up] followed by the block Hadamard transform");
   m.def("glu", &glu_act, "act(gate) * up of [gate; up]: act 0 = SiLU, 1 = GELU (tanh approximation), 2 = clamped "
         "SwiGLU with the given limit", py::arg("gu"), py::arg("act"), py::arg("limit") = 7.0);
   m.def("linear_parts", &linear_parts, "x @ w.T as bf16 or fp32 split-K partials for a fusing consumer");

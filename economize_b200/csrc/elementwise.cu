@@ -356,6 +356,107 @@ int launch_silu_mul(const void* gu, void* out, int rows, int F, cudaStream_t str
 }
 
 // ---------------------------------------------------------------------------------------------------------------
+// Block Walsh-Hadamard transform along the last dimension (QuaRot's online rotation of the down projection's input):
+// y[r, k*b : (k+1)*b] = x[r, k*b : (k+1)*b] H_b / sqrt(b) with H_b the Sylvester matrix, b a power of two in
+// [8, kMaxHadamard]. kGlu = true computes x as act(gate) * up of a fused [gate; up] projection first (the producing
+// kernel of the rotated activation, so the activation never goes through HBM unrotated); its bf16 rounding is that of
+// glu_kernel, so the fused result equals glu followed by the plain transform bit for bit.
+//
+// One CTA of 256 threads per (row, block): each thread loads 8 consecutive elements (16-byte loads), applies the
+// butterflies of half-width 1, 2 and 4 in registers, and stores them to shared memory (b fp32 values); the butterflies
+// of half-width 8 .. b/2 then run in shared memory, one __syncthreads() per stage; the result is scaled and stored with
+// 16-byte stores. The transform is memory bound (b x 2 bytes in and out per CTA); stages run in the order h = 1, 2, 4,
+// ..., b/2, the order of the fp32 host reference.
+// ---------------------------------------------------------------------------------------------------------------
+constexpr int kMaxHadamard = 8192;  // 32 KB of fp32 shared memory: below the 48 KB default, no attribute needed
+
+template <int kAct, bool kGlu>
+__global__ void __launch_bounds__(256) hadamard_kernel(const bf16* __restrict__ in, bf16* __restrict__ out, int F,
+                                                       int block, int blocks_per_row, Parts parts, float limit,
+                                                       float scale) {
+  extern __shared__ float hsh[];
+  pdl_trigger();
+  pdl_wait();
+  const int r = blockIdx.x / blocks_per_row;
+  const int base = (blockIdx.x % blocks_per_row) * block;
+  const int groups = block / 8;
+  for (int g = threadIdx.x; g < groups; g += blockDim.x) {
+    float v[8];
+    if constexpr (kGlu) {
+      const size_t off = static_cast<size_t>(r) * 2 * F + base + g * 8;
+      const uint4 gv = load8(in, parts, off);
+      const uint4 uv = load8(in, parts, off + F);
+      const bf16* gp = reinterpret_cast<const bf16*>(&gv);
+      const bf16* up = reinterpret_cast<const bf16*>(&uv);
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        const float a = bf16r(glu_act<kAct>(__bfloat162float(gp[j]), limit));
+        v[j] = bf16r(a * glu_up<kAct>(__bfloat162float(up[j]), limit));
+      }
+    } else {
+      const uint4 xv = *reinterpret_cast<const uint4*>(in + static_cast<size_t>(r) * F + base + g * 8);
+      const bf16* xp = reinterpret_cast<const bf16*>(&xv);
+#pragma unroll
+      for (int j = 0; j < 8; ++j) v[j] = __bfloat162float(xp[j]);
+    }
+#pragma unroll
+    for (int h = 1; h < 8; h <<= 1) {
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        if ((j & h) == 0) {
+          const float a = v[j], b = v[j + h];
+          v[j] = a + b;
+          v[j + h] = a - b;
+        }
+      }
+    }
+    float4* dst = reinterpret_cast<float4*>(hsh + g * 8);
+    dst[0] = make_float4(v[0], v[1], v[2], v[3]);
+    dst[1] = make_float4(v[4], v[5], v[6], v[7]);
+  }
+  __syncthreads();
+  for (int h = 8; h < block; h <<= 1) {
+    for (int t = threadIdx.x; t < block / 2; t += blockDim.x) {
+      const int i = ((t & ~(h - 1)) << 1) | (t & (h - 1));
+      const float a = hsh[i], b = hsh[i + h];
+      hsh[i] = a + b;
+      hsh[i + h] = a - b;
+    }
+    __syncthreads();
+  }
+  for (int g = threadIdx.x; g < groups; g += blockDim.x) {
+    const float4 a = reinterpret_cast<const float4*>(hsh + g * 8)[0];
+    const float4 b = reinterpret_cast<const float4*>(hsh + g * 8)[1];
+    uint4 o;
+    __nv_bfloat162* op = reinterpret_cast<__nv_bfloat162*>(&o);
+    op[0] = __floats2bfloat162_rn(a.x * scale, a.y * scale);
+    op[1] = __floats2bfloat162_rn(a.z * scale, a.w * scale);
+    op[2] = __floats2bfloat162_rn(b.x * scale, b.y * scale);
+    op[3] = __floats2bfloat162_rn(b.z * scale, b.w * scale);
+    *reinterpret_cast<uint4*>(out + static_cast<size_t>(r) * F + base + g * 8) = o;
+  }
+}
+
+int launch_hadamard(const void* x, void* out, int rows, int F, int block, cudaStream_t stream, int glu_act_kind,
+                    const float* gu_parts, int splits, float limit) {
+  if (block < 8 || block > kMaxHadamard || (block & (block - 1)) != 0 || F % block != 0 || rows < 1) return -1;
+  if (glu_act_kind < -1 || glu_act_kind > 2) return -1;
+  const long ctas = static_cast<long>(rows) * (F / block);
+  if (ctas > 0x7fffffffL) return -1;
+  const Parts parts{gu_parts, splits, static_cast<long>(rows) * 2 * F};
+  const size_t smem = static_cast<size_t>(block) * sizeof(float);
+  const float scale = rsqrtf(static_cast<float>(block));
+  auto kernel = glu_act_kind < 0    ? hadamard_kernel<0, false>
+                : glu_act_kind == 0 ? hadamard_kernel<0, true>
+                : glu_act_kind == 1 ? hadamard_kernel<1, true>
+                                    : hadamard_kernel<2, true>;
+  const cudaError_t err = launch_pdl(kernel, dim3(static_cast<unsigned>(ctas)), dim3(256), smem, stream,
+                                     static_cast<const bf16*>(x), static_cast<bf16*>(out), F, block, F / block, parts,
+                                     limit, scale);
+  return err == cudaSuccess ? 0 : -3;
+}
+
+// ---------------------------------------------------------------------------------------------------------------
 // Row argmax (first maximal index), bf16 or fp32 input
 // ---------------------------------------------------------------------------------------------------------------
 template <typename T>

@@ -98,6 +98,11 @@ int launch_glu(const void* gu, void* out, int rows, int F, cudaStream_t stream, 
                float limit = 7.f);
 int launch_silu_mul(const void* gu, void* out, int rows, int F, cudaStream_t stream, const float* gu_parts = nullptr,
                     int splits = 0);
+// Block Walsh-Hadamard transform x H_b / sqrt(b) of every row (blocks of b = 2^p, 8 <= b <= 8192, dividing F); with
+// glu_act_kind >= 0 the input is the fused [gate; up] projection and the transformed value is act(gate) * up
+// (glu_act_kind as launch_glu's act; -1: x is the bf16 [rows, F] input itself)
+int launch_hadamard(const void* x, void* out, int rows, int F, int block, cudaStream_t stream, int glu_act_kind = -1,
+                    const float* gu_parts = nullptr, int splits = 0, float limit = 7.f);
 int argmax_slices(int rows, int V);
 int launch_argmax(const void* x, bool is_bf16, int64_t* out, float* part_v, int* part_i, int rows, int V,
                   cudaStream_t stream);

@@ -190,5 +190,16 @@ def export_hf_state(model, copy: bool = True) -> dict[str, torch.Tensor]:
             g, u = full(layer.w_gate_up).chunk(2, 0)
             out[p + "mlp.gate_proj.weight"] = g
             out[p + "mlp.up_proj.weight"] = u
-            out[p + "mlp.down_proj.weight"] = full(layer.w_down)
+            out[p + "mlp.down_proj.weight"] = _unrotated_down(layer, full(layer.w_down))
     return {k: v.clone() for k, v in out.items()} if copy else out
+
+
+def _unrotated_down(layer, weight: torch.Tensor) -> torch.Tensor:
+    """``w_down`` as a model without the online Hadamard rotation needs it: the rotate technique stores ``W H`` and
+    rotates the input online; ``H`` (block-diagonal normalized Sylvester) is its own inverse, so ``W = (W H) H``."""
+    block = getattr(layer, "down_hadamard", 0)
+    if not block:
+        return weight
+    from ..ops import reference
+
+    return reference.hadamard(weight.float(), block).to(weight.dtype)

@@ -38,6 +38,9 @@ class DecoderLayer(nn.Module):
         super().__init__()
         h, f = config.hidden_size, config.intermediate_size
         kw = dict(dtype=dtype, device=device)
+        #: block size of the online Hadamard rotation of the down projection's input (0: none); set by the
+        #: rotate technique, which folds the same rotation into w_down
+        self.down_hadamard = 0
         self.attn_norm = nn.Parameter(torch.ones(h, **kw))
         self.wqkv = nn.Parameter(torch.empty(config.q_size + 2 * config.kv_size, h, **kw))
         self.bqkv = nn.Parameter(torch.zeros(config.q_size + 2 * config.kv_size, **kw)) if config.attention_bias \
@@ -384,7 +387,8 @@ class CausalLM(nn.Module):
             o = self._attend(layer, i, qkv, batch, cache, cos, sin)
             sp.rs_linear(o, layer.wo)
             resid = sp.reduce_norm(resid, layer.mlp_norm, eps, M)
-            a = ops.silu_mul(sp.ag_linear_parts(layer.w_gate_up, M, (M,)))
+            a = ops.glu(sp.ag_linear_parts(layer.w_gate_up, M, (M,)), self.config.hidden_act,
+                        self.config.swiglu_limit, hadamard=layer.down_hadamard)
             sp.rs_linear(a, layer.w_down)
             nxt = self.layers[i + 1].attn_norm if i + 1 < len(self.layers) else self.norm
             resid = sp.reduce_norm(resid, nxt, eps, M, capture=slot_of.get(i + 1, -1))
@@ -529,7 +533,8 @@ class CausalLM(nn.Module):
             out = rule(self, layer, x, index)
             if out is not None:
                 return out
-        a = ops.glu(self._linear(x, layer.w_gate_up), self.config.hidden_act, self.config.swiglu_limit)
+        a = ops.glu(self._linear(x, layer.w_gate_up), self.config.hidden_act, self.config.swiglu_limit,
+                    hadamard=layer.down_hadamard)
         if self.observer is not None:
             self.observer(index, "w_down", a)
         return self._row_linear(a, layer.w_down)

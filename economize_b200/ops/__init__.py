@@ -38,6 +38,7 @@ __all__ = [
     "topk_logp",
     "tree_layout",
     "silu_mul",
+    "hadamard",
     "gelu_tanh_mul",
     "glu",
 ]
@@ -221,10 +222,29 @@ def gelu_tanh_mul(gate_up: torch.Tensor | Partials) -> torch.Tensor:
     return reference.gelu_tanh_mul(gate_up.sum() if isinstance(gate_up, Partials) else gate_up)
 
 
-def glu(gate_up: torch.Tensor | Partials, act: str = "silu", limit: float = 7.0) -> torch.Tensor:
+_GLU_ACTS = {"silu": 0, "gelu_tanh": 1, "clamped_swiglu": 2}
+
+
+def hadamard(x: torch.Tensor, block: int) -> torch.Tensor:
+    """``x H_b / sqrt(b)`` over consecutive blocks of ``block`` (a power of two) of the last dimension: QuaRot's
+    online rotation. On CUDA (bf16, ``8 <= block <= 8192``) the kernel of ``csrc/elementwise.cu:hadamard_kernel``."""
+    if x.is_cuda and x.dtype == torch.bfloat16:
+        return require().hadamard(x, block)
+    return reference.hadamard(x, block)
+
+
+def glu(gate_up: torch.Tensor | Partials, act: str = "silu", limit: float = 7.0, hadamard: int = 0) -> torch.Tensor:
     """The gated MLP activation ``act(gate) * up`` (``"silu"``: SwiGLU, ``"gelu_tanh"``: GeGLU,
     ``"clamped_swiglu"``: gpt-oss's ``(clamp(up, +-limit) + 1) * g * sigmoid(1.702 g)`` with ``g = min(gate,
-    limit)``)."""
+    limit)``). ``hadamard > 0`` rotates the result by the block Hadamard transform of that block size in the same
+    kernel (on CUDA), the online input rotation of a rotated down projection."""
+    if hadamard:
+        if act not in _GLU_ACTS:
+            raise ValueError(f"unsupported gated activation {act!r}")
+        if gate_up.is_cuda and (isinstance(gate_up, Partials) or gate_up.dtype == torch.bfloat16):
+            return require().glu_hadamard(_raw(gate_up), _GLU_ACTS[act], limit, hadamard)
+        dense = gate_up.sum() if isinstance(gate_up, Partials) else gate_up
+        return reference.hadamard(reference.glu(dense, act, limit), hadamard)
     if act == "silu":
         return silu_mul(gate_up)
     if act == "gelu_tanh":

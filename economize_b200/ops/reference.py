@@ -223,6 +223,22 @@ def glu(gate_up: torch.Tensor, act: str = "silu", limit: float = 7.0) -> torch.T
     raise ValueError(f"unsupported gated activation {act!r}")
 
 
+def hadamard(x: torch.Tensor, block: int) -> torch.Tensor:
+    """``x H_b / sqrt(b)`` over consecutive blocks of ``block`` (a power of two) of the last dimension, with ``H_b``
+    the Sylvester matrix: the fast Walsh-Hadamard transform in fp32, butterflies of half-width 1, 2, 4, ... (the
+    order of the CUDA kernel), rounded once to ``x``'s dtype."""
+    if block < 1 or block & (block - 1) or x.shape[-1] % block:
+        raise ValueError(f"hadamard block {block} must be a power of two dividing the width {x.shape[-1]}")
+    work = x.float().reshape(-1, block)
+    h = 1
+    while h < block:
+        pairs = work.view(-1, block // (2 * h), 2, h)
+        a, b = pairs[:, :, 0], pairs[:, :, 1]
+        work = torch.stack((a + b, a - b), dim=2).reshape(-1, block)
+        h *= 2
+    return (work * block ** -0.5).reshape(x.shape).to(x.dtype)
+
+
 def linear(x: torch.Tensor, weight: torch.Tensor, bias: torch.Tensor | None = None) -> torch.Tensor:
     return F.linear(x, weight, bias)
 

@@ -89,6 +89,9 @@ def shard_model(model, tp: TPGroup):
             layer.sinks.data = layer.sinks.data[r * hq:(r + 1) * hq].contiguous()
         gate, up = layer.w_gate_up.data.chunk(2, 0)
         layer.w_gate_up.data = torch.cat([gate[r * f:(r + 1) * f], up[r * f:(r + 1) * f]], 0).contiguous()
+        if layer.down_hadamard and f % layer.down_hadamard:
+            raise ConfigError(f"the online Hadamard block {layer.down_hadamard} of the down projection does not "
+                              f"divide the per-rank width {f}; rotate with a smaller block")
         layer.w_down.data = layer.w_down.data[:, r * f:(r + 1) * f].contiguous()
     if model.lm_head is None:
         model.lm_head = torch.nn.Parameter(model.embed.data[r * v:(r + 1) * v].clone())

@@ -196,6 +196,10 @@ class _MlpSparsityBase(Technique):
         self.masked = []
         for li, i in enumerate(self.layer_ids):
             layer = self.model.layers[i]
+            if layer.down_hadamard:
+                self.detach()
+                raise ConfigError(f"{self.name}: layer {i + 1}'s down projection reads an online-rotated input "
+                                  "(rotate with online=()) and the sparse MLP kernels compute it unrotated")
             reason = _eligible(layer.w_gate_up) or _eligible(layer.w_down)
             if cfg.backend == "auto" and reason is not None:
                 self.detach()

@@ -239,7 +239,12 @@ def torch_block(layer, h: torch.Tensor, config, cos: torch.Tensor, sin: torch.Te
     h = h + lin(o.transpose(1, 2).reshape(batch, length, heads * hd), layer.wo)
     x = rmsnorm(h, layer.mlp_norm, eps)[0]
     g, u = lin(x, layer.w_gate_up).chunk(2, -1)
-    return h + lin(F.silu(g) * u, layer.w_down)
+    a = F.silu(g) * u
+    if layer.down_hadamard:  # the online rotation the rotate technique folded into w_down
+        from ..ops import reference
+
+        a = reference.hadamard(a, layer.down_hadamard)
+    return h + lin(a, layer.w_down)
 
 
 @OBJECTIVES.register("recovery_ce")
