@@ -438,6 +438,32 @@ Tensor glu_act(Tensor gu, int64_t act, double limit) {
 
 Tensor silu_mul(Tensor gu) { return glu_act(gu, 0, 0.0); }
 
+// MInference vertical-slash pattern -> keep bit words: cols [..., nv], offsets [..., ns] (int64, same leading shape)
+Tensor vs_keep(Tensor cols, Tensor offsets, int64_t base, int64_t t, int64_t limit, int64_t S) {
+  CHECK_CUDA(cols);
+  CHECK_ON(offsets, cols);
+  TORCH_CHECK(cols.scalar_type() == at::kLong && offsets.scalar_type() == at::kLong, "vs_keep: int64 indices");
+  TORCH_CHECK(cols.dim() >= 1 && offsets.dim() == cols.dim() &&
+                  cols.sizes().slice(0, cols.dim() - 1) == offsets.sizes().slice(0, offsets.dim() - 1),
+              "vs_keep: cols [..., nv] and offsets [..., ns] with the same leading shape");
+  c10::cuda::CUDAGuard guard(cols.device());
+  cols = cols.contiguous();
+  offsets = offsets.contiguous();
+  const int nv = static_cast<int>(cols.size(-1)), ns = static_cast<int>(offsets.size(-1));
+  const int rows = nv ? static_cast<int>(cols.numel() / nv) : static_cast<int>(offsets.numel() / std::max(ns, 1));
+  auto shape = cols.sizes().vec();
+  shape.back() = S / 32;
+  auto keep = at::empty(shape, cols.options().dtype(at::kInt));
+  if (rows == 0) return keep;
+  const int rc = ecz::launch_vs_keep(cols.data_ptr<int64_t>(), nv, offsets.data_ptr<int64_t>(), ns,
+                                     static_cast<int>(base), static_cast<int>(t), static_cast<int>(limit), rows,
+                                     static_cast<int>(S), reinterpret_cast<uint32_t*>(keep.data_ptr<int>()),
+                                     at::cuda::getCurrentCUDAStream());
+  TORCH_CHECK(rc != -3, "vs_keep: the kernel launch was refused: ", cudaGetErrorString(cudaGetLastError()));
+  TORCH_CHECK(rc == 0, "vs_keep: S must be a multiple of 32 and at most 262144, got ", S);
+  return keep;
+}
+
 // Block Walsh-Hadamard transform of the last dimension of a bf16 tensor (blocks of `block`, a power of two in
 // [8, 8192] dividing the width), scaled by 1 / sqrt(block)
 Tensor hadamard(Tensor x, int64_t block) {
@@ -1522,6 +1548,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
         py::arg("k_cache"), py::arg("kv_len"), py::arg("n_new"), py::arg("mask"), py::arg("lse2"), py::arg("scores"),
         py::arg("scale"), py::arg("q_offset"), py::arg("pages") = py::none());
   m.def("silu_mul", &silu_mul, "SwiGLU activation of [gate; up]");
+  m.def("vs_keep", &vs_keep, "MInference vertical-slash pattern -> per-KV-head keep bit words");
   m.def("hadamard", &hadamard, "block Walsh-Hadamard transform of the last dimension (QuaRot online rotation)");
   m.def("glu_hadamard", &glu_hadamard, "act(gate) * up of [gate; up] followed by the block Hadamard transform");
   m.def("glu", &glu_act, "act(gate) * up of [gate; up]: act 0 = SiLU, 1 = GELU (tanh approximation), 2 = clamped "

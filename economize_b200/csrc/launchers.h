@@ -103,6 +103,11 @@ int launch_silu_mul(const void* gu, void* out, int rows, int F, cudaStream_t str
 // (glu_act_kind as launch_glu's act; -1: x is the bf16 [rows, F] input itself)
 int launch_hadamard(const void* x, void* out, int rows, int F, int block, cudaStream_t stream, int glu_act_kind = -1,
                     const float* gu_parts = nullptr, int splits = 0, float limit = 7.f);
+// MInference vertical-slash keep bitmap of `rows` (row, KV head) pairs: cols [rows, nv] key columns, offsets [rows, ns]
+// slash diagonals (query position - key position) of a chunk of t queries at `base`; keys >= limit are dropped;
+// keep [rows, S / 32] bit words (S a multiple of 32, at most 262144)
+int launch_vs_keep(const int64_t* cols, int nv, const int64_t* offsets, int ns, int base, int t, int limit, int rows,
+                   int S, uint32_t* keep, cudaStream_t stream);
 int argmax_slices(int rows, int V);
 int launch_argmax(const void* x, bool is_bf16, int64_t* out, float* part_v, int* part_i, int rows, int V,
                   cudaStream_t stream);

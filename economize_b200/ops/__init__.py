@@ -39,6 +39,7 @@ __all__ = [
     "tree_layout",
     "silu_mul",
     "hadamard",
+    "vs_keep",
     "gelu_tanh_mul",
     "glu",
 ]
@@ -223,6 +224,15 @@ def gelu_tanh_mul(gate_up: torch.Tensor | Partials) -> torch.Tensor:
 
 
 _GLU_ACTS = {"silu": 0, "gelu_tanh": 1, "clamped_swiglu": 2}
+
+
+def vs_keep(cols: torch.Tensor, offsets: torch.Tensor, base: int, t: int, limit: int, size: int) -> torch.Tensor:
+    """MInference's vertical-slash pattern of a query chunk (``t`` queries from position ``base``) as keep bit words
+    ``int32 [..., size / 32]`` for the attention kernel: key columns ``cols [..., nv]`` and the keys that the slash
+    diagonals ``offsets [..., ns]`` cross, below ``limit``. On CUDA ``csrc/minference.cu:vs_keep_kernel``."""
+    if cols.is_cuda:
+        return require().vs_keep(cols.long(), offsets.long(), base, t, limit, size)
+    return reference.vs_keep(cols.long(), offsets.long(), base, t, limit, size)
 
 
 def hadamard(x: torch.Tensor, block: int) -> torch.Tensor:

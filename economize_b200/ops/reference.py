@@ -223,6 +223,26 @@ def glu(gate_up: torch.Tensor, act: str = "silu", limit: float = 7.0) -> torch.T
     raise ValueError(f"unsupported gated activation {act!r}")
 
 
+def vs_keep(cols: torch.Tensor, offsets: torch.Tensor, base: int, t: int, limit: int, size: int) -> torch.Tensor:
+    """MInference's vertical-slash pattern as keep bit words ``int32 [..., size / 32]``: key ``j < limit`` is kept
+    when it is one of ``cols`` or lies in ``[base - o, base + t - o)`` for a diagonal offset ``o`` of ``offsets``.
+    The diagonals' union is a difference array and a prefix sum (memory ``O(size)``, not ``O(ns * size)``)."""
+    lead = cols.shape[:-1]
+    cols2, offs = cols.reshape(-1, cols.shape[-1]), offsets.reshape(-1, offsets.shape[-1])
+    rows = cols2.shape[0]
+    diff = torch.zeros(rows, size + 1, dtype=torch.int32, device=cols.device)
+    ones = torch.ones_like(offs, dtype=torch.int32)
+    diff.scatter_add_(1, (base - offs).clamp(0, size), ones)
+    diff.scatter_add_(1, (base + t - offs).clamp(0, size), -ones)
+    keep = diff.cumsum(1)[:, :size] > 0
+    valid = (cols2 >= 0) & (cols2 < size)
+    keep.scatter_(1, cols2.clamp(0, size - 1), valid | keep.gather(1, cols2.clamp(0, size - 1)))
+    keep &= torch.arange(size, device=cols.device)[None] < limit
+    bits = keep.reshape(rows, size // 32, 32).to(torch.int64)
+    words = (bits << torch.arange(32, device=cols.device)).sum(-1)
+    return torch.where(words >= 2 ** 31, words - 2 ** 32, words).to(torch.int32).reshape(*lead, size // 32)
+
+
 def hadamard(x: torch.Tensor, block: int) -> torch.Tensor:
     """``x H_b / sqrt(b)`` over consecutive blocks of ``block`` (a power of two) of the last dimension, with ``H_b``
     the Sylvester matrix: the fast Walsh-Hadamard transform in fp32, butterflies of half-width 1, 2, 4, ... (the

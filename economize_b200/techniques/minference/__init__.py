@@ -24,6 +24,7 @@ from typing import ClassVar
 
 import torch
 
+from ... import ops
 from ...core.technique import Capability, Family, Technique, TechniqueConfig, register_technique
 from ...errors import ConfigError
 from ...runtime.cache import StepBatch
@@ -118,7 +119,7 @@ class MInferencePrefill:
             keep |= (pos < c.sinks)[None, None]
             keep |= ((pos >= base - c.local) & (pos < base))[None, None]
         elif c.pattern == "vertical_slash":
-            keep |= self._vertical_slash(k_cache, q, base, t)
+            return self._vertical_slash(k_cache, q, base, t)
         else:
             keep |= self._block_sparse(k_cache, q, base)
         return keep_words(keep)
@@ -145,12 +146,10 @@ class MInferencePrefill:
         last = min(64, t)
         probs, qpos = self._scores(k_cache, q, base, last)  # [B, Hkv, G L, S']
         width = probs.shape[-1]
-        keep = torch.zeros(b, hkv, s, dtype=torch.bool, device=dev)
         nv = min(width, max(int(c.vertical * c.ratio), 30))
         vert = probs.sum(2)  # [B, Hkv, S']
         vert[..., :30] = float("inf")  # the first 30 columns always stay
         cols = vert.topk(nv, -1).indices
-        keep.scatter_(2, cols, True)
         # diagonals: offset o = q - k, summed over the estimating queries
         g = self.group
         off = (qpos.repeat(g)[:, None] - torch.arange(width, device=dev)[None])  # [G L, S']
@@ -161,12 +160,9 @@ class MInferencePrefill:
         slash[..., :100] = float("inf")  # the 100 diagonals nearest the main one
         ns = min(width, max(int(c.slash * c.ratio), 50))
         offsets = slash.topk(ns, -1).indices  # [B, Hkv, ns]
-        # a diagonal o crosses keys [base - o, base + t - o) for the chunk's queries
-        lo = (base - offsets).clamp_min(0)
-        hi = (base + t - offsets).clamp(0, s)
-        span = torch.arange(s, device=dev)[None, None, None]
-        keep |= ((span >= lo[..., None]) & (span < hi[..., None])).any(2)
-        return keep
+        # columns and the keys [base - o, base + t - o) each diagonal crosses for the chunk's queries, as bit words
+        # (a kernel on CUDA); only keys before the chunk are read through the pattern
+        return ops.vs_keep(cols, offsets, base, t, base, s)
 
     def _block_sparse(self, k_cache, q, base: int) -> torch.Tensor:
         c = self.config

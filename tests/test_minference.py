@@ -65,3 +65,49 @@ def test_sparse_prefill_on_gpu_matches_reference_attention(cuda):
     assert rel < 0.05, float(rel)
     dense = _hidden(gpu_tiny_model(cuda), tokens).cpu()
     assert (h - dense).norm() / dense.norm() > 2 * rel  # the pattern did hide keys
+
+
+def _naive_vs_keep(cols, offsets, base, t, limit, size):
+    keep = torch.zeros(*cols.shape[:-1], size, dtype=torch.bool)
+    j = torch.arange(size)
+    for idx in torch.cartesian_prod(*[torch.arange(n) for n in cols.shape[:-1]]).reshape(-1, cols.dim() - 1):
+        idx = tuple(idx.tolist())
+        row = torch.zeros(size, dtype=torch.bool)
+        for c in cols[idx].tolist():
+            if 0 <= c < size:
+                row[c] = True
+        for o in offsets[idx].tolist():
+            row |= (j >= base - o) & (j < base + t - o)
+        keep[idx] = row & (j < limit)
+    return keep
+
+
+def _bits(words, size):
+    return ((words.long()[..., None] >> torch.arange(32)) & 1).bool().reshape(*words.shape[:-1], size)
+
+
+def test_vs_keep_reference_matches_the_definition():
+    from economize_b200.ops import reference
+
+    g = torch.Generator().manual_seed(0)
+    size, base, t = 512, 300, 64
+    cols = torch.randint(-3, size + 5, (2, 3, 40), generator=g)
+    offsets = torch.randint(-10, 400, (2, 3, 25), generator=g)
+    for limit in (base, 129, 0):
+        got = _bits(reference.vs_keep(cols, offsets, base, t, limit, size), size)
+        assert torch.equal(got, _naive_vs_keep(cols, offsets, base, t, limit, size))
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("size,nv,ns", [(512, 40, 25), (131072, 1000, 1000), (4096, 0, 64), (2048, 30, 0)])
+def test_vs_keep_kernel_matches_reference(cuda, size, nv, ns):
+    from economize_b200 import ops
+    from economize_b200.ops import reference
+
+    g = torch.Generator().manual_seed(size + nv)
+    base, t = size - size // 4, min(2048, size // 4)
+    cols = torch.randint(-3, size + 5, (2, 8, nv), generator=g)
+    offsets = torch.randint(-10, size, (2, 8, ns), generator=g)
+    for limit in (base, base - 7):
+        got = ops.vs_keep(cols.to(cuda), offsets.to(cuda), base, t, limit, size)
+        assert torch.equal(got.cpu(), reference.vs_keep(cols, offsets, base, t, limit, size))
