@@ -450,7 +450,9 @@ Tensor vs_keep(Tensor cols, Tensor offsets, int64_t base, int64_t t, int64_t lim
   cols = cols.contiguous();
   offsets = offsets.contiguous();
   const int nv = static_cast<int>(cols.size(-1)), ns = static_cast<int>(offsets.size(-1));
-  const int rows = nv ? static_cast<int>(cols.numel() / nv) : static_cast<int>(offsets.numel() / std::max(ns, 1));
+  int64_t rows64 = 1;
+  for (int64_t d = 0; d + 1 < cols.dim(); ++d) rows64 *= cols.size(d);
+  const int rows = static_cast<int>(rows64);
   auto shape = cols.sizes().vec();
   shape.back() = S / 32;
   auto keep = at::empty(shape, cols.options().dtype(at::kInt));

@@ -228,8 +228,10 @@ def vs_keep(cols: torch.Tensor, offsets: torch.Tensor, base: int, t: int, limit:
     when it is one of ``cols`` or lies in ``[base - o, base + t - o)`` for a diagonal offset ``o`` of ``offsets``.
     The diagonals' union is a difference array and a prefix sum (memory ``O(size)``, not ``O(ns * size)``)."""
     lead = cols.shape[:-1]
-    cols2, offs = cols.reshape(-1, cols.shape[-1]), offsets.reshape(-1, offsets.shape[-1])
-    rows = cols2.shape[0]
+    rows = 1
+    for n in lead:
+        rows *= n
+    cols2, offs = cols.reshape(rows, cols.shape[-1]), offsets.reshape(rows, offsets.shape[-1])
     diff = torch.zeros(rows, size + 1, dtype=torch.int32, device=cols.device)
     ones = torch.ones_like(offs, dtype=torch.int32)
     diff.scatter_add_(1, (base - offs).clamp(0, size), ones)
