@@ -208,16 +208,25 @@ class JumpTechnique(Technique):
 
 @OBJECTIVES.register("jump_rollout")
 class JumpRollout(Objective):
-    """Normalised squared error between the predicted and the target's state after layer ``m`` at ``t + 1``."""
+    """``horizon=1``: normalised squared error between the predicted and the target's state after layer ``m`` at
+    ``t + 1``, from the target's own sources (teacher forcing). ``horizon > 1``: open-loop rollouts
+    (:func:`~.rollout.rollout_steps`): step ``j`` of the rollout from every start ``p`` predicts position ``p + j``
+    from the states the drafter itself produced at step ``j - 1``; each step's loss is the state error against the
+    target's state after layer ``m`` at ``p + j`` plus ``ce_weight`` times the cross-entropy of the step's logits
+    against the target's greedy token after ``p + j``, and step ``j`` weighs ``decay**(j - 1)``."""
 
     name = "jump_rollout"
     defaults = OptimDefaults(lr=1e-3, warmup_steps=0)
 
-    def __init__(self, model) -> None:
+    def __init__(self, model, horizon: int = 1, ce_weight: float = 1.0, decay: float = 0.8) -> None:
         super().__init__(model)
         if "jump" not in model.techniques:
             raise ConfigError("jump_rollout needs an attached jump technique")
+        check_positive("horizon", horizon)
+        if ce_weight < 0 or not 0 < decay <= 1:
+            raise ConfigError(f"jump_rollout needs ce_weight >= 0 and 0 < decay <= 1, got {ce_weight}, {decay}")
         self.tech = model.techniques["jump"]
+        self.horizon, self.ce_weight, self.decay = int(horizon), float(ce_weight), float(decay)
 
     def parameters(self):
         return list(self.tech.predictor.parameters()) + list(self.tech.mixer.parameters())
@@ -225,15 +234,43 @@ class JumpRollout(Objective):
     def loss(self, tokens: torch.Tensor):
         tech = self.tech
         model = tech.model
-        m, u, _ = tech.layers
+        m, _, r = tech.layers
         b, s = tokens.shape
+        capture = (m, *tech.sources) if self.horizon == 1 else tuple(sorted({*range(m, r + 1), *tech.sources}))
         with torch.no_grad():
             cache = model.new_cache(b, ((s + 127) // 128) * 128)
             lengths = torch.full((b,), s, dtype=torch.int32, device=tokens.device)
-            _, aux = model.forward_step(tokens, StepBatch.prefill(lengths, s), cache, capture=(m, *tech.sources))
+            final, aux = model.forward_step(tokens, StepBatch.prefill(lengths, s), cache, capture=capture)
             emb = model.embed_tokens(tokens)
-        pred = tech.predictor(tech.mix(aux)[:, :-1].float(), emb[:, 1:].float())
-        target = aux[m][:, 1:].float()
-        err = (pred.float() - target).pow(2).sum(-1) / target.pow(2).sum(-1).clamp_min(1e-6)
-        loss = err.mean()
-        return loss, {"loss": float(loss.detach())}
+        if self.horizon == 1:
+            pred = tech.predictor(tech.mix(aux)[:, :-1].float(), emb[:, 1:].float())
+            target = aux[m][:, 1:].float()
+            err = (pred.float() - target).pow(2).sum(-1) / target.pow(2).sum(-1).clamp_min(1e-6)
+            loss = err.mean()
+            return loss, {"loss": float(loss.detach())}
+        from ...ops import reference
+        from ...train.objective import dense_linear
+        from .rollout import rollout_steps
+
+        with torch.no_grad():
+            labels = model.logits(final).argmax(-1)  # the target's greedy token after every position
+        starts, steps = rollout_steps(tech, tokens, aux, self.horizon)
+        total, weight, stats = 0.0, 0.0, {}
+        for j, (h_m, h_r) in enumerate(steps, start=1):
+            pos = starts + j
+            target = aux[m][:, pos].float()
+            err = ((h_m.float() - target).pow(2).sum(-1) / target.pow(2).sum(-1).clamp_min(1e-6)).mean()
+            step_loss = err
+            if self.ce_weight:
+                x = reference.rmsnorm(h_r, model.norm, model.config.rms_norm_eps)[0]
+                logits = dense_linear(x, model.head_weight, None).float() / model.config.logits_scaling
+                ce = F.cross_entropy(logits.reshape(-1, logits.shape[-1]), labels[:, pos].reshape(-1))
+                step_loss = step_loss + self.ce_weight * ce
+                stats[f"ce_{j}"] = float(ce.detach())
+            w = self.decay ** (j - 1)
+            total = total + w * step_loss
+            weight += w
+            stats[f"state_{j}"] = float(err.detach())
+        loss = total / weight
+        stats["loss"] = float(loss.detach())
+        return loss, stats

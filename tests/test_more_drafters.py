@@ -189,3 +189,66 @@ def test_jump_mixers_start_on_the_last_source():
             assert torch.equal(a.tokens, b.tokens) and a.accepted == b.accepted
     with pytest.raises(eco.ConfigError, match="source_layers"):
         eco.apply(tiny_model(), JC(target_layer=2, source_layers=(1, 3)))
+
+
+@pytest.mark.parametrize("cfg", [JumpConfig(target_layer=1, source_layer=2, exit_layer=4),
+                                 JumpConfig(target_layer=1, source_layers=(1, 3), mixer="concat", exit_layer=3),
+                                 JumpConfig(target_layer=2, source_layers=(2, 4), mixer="attention")])
+def test_jump_rollout_matches_the_drafter(cfg):
+    """Every step of the training rollout reproduces what the drafter computes at decode time from the same start:
+    the same predicted states, the same partial passes against the exact and its own keys, the same logits."""
+    from economize_b200.runtime.cache import StepBatch
+    from economize_b200.ops import reference
+    from economize_b200.techniques.jump.rollout import rollout_steps
+
+    em = eco.apply(tiny_model(), cfg)
+    tech = em.techniques["jump"]
+    g = torch.Generator().manual_seed(7)
+    with torch.no_grad():  # a predictor away from its identity start, so the rollout's own states matter
+        for p in tech.predictor.parameters():
+            p.add_(torch.randn(p.shape, generator=g) * 0.05)
+        for p in tech.mixer.parameters():
+            p.add_(torch.randn(p.shape, generator=g) * 0.05)
+    model = em.model
+    tokens = torch.randint(0, 1024, (1, 24), generator=g)
+    m, _, r = tech.layers
+    capture = tuple(sorted({*range(m, r + 1), *tech.sources}))
+    with torch.no_grad():
+        cache = model.new_cache(1, 128)
+        _, aux = model.forward_step(tokens, StepBatch.prefill(torch.tensor([24], dtype=torch.int32), 24), cache,
+                                    capture=capture)
+        starts, steps = rollout_steps(tech, tokens, aux, 3)
+    assert starts.tolist() == list(range(21))
+    drafter = tech.drafter()
+    for start in (0, 9, 20):
+        with torch.no_grad():
+            exact = model.new_cache(1, 128)
+            _, ex = model.forward_step(tokens[:, :start + 1], StepBatch.prefill(
+                torch.tensor([start + 1], dtype=torch.int32), start + 1), exact, capture=tech.sources)
+            drafter.bind_target_cache(exact)
+            source = tech.mix(ex)[:, start:start + 1].to(model.dtype)
+            for j in range(1, 4):
+                slot = torch.tensor([start + j], dtype=torch.int32)
+                logits, source = drafter._run(tokens[:, start + j:start + j + 1], source,
+                                              StepBatch(slot, torch.ones(1, dtype=torch.int32), slot[:, None]))
+                normed = reference.rmsnorm(steps[j - 1][1][:, start:start + 1], model.norm,
+                                           model.config.rms_norm_eps)[0]
+                want = model.logits(normed)
+                torch.testing.assert_close(logits, want.float(), atol=2e-4, rtol=1e-4)
+
+
+def test_jump_open_loop_objective_trains():
+    em = eco.apply(tiny_model(), JumpConfig(target_layer=1, source_layer=2))
+    obj = OBJECTIVES.get("jump_rollout")(em, horizon=3, ce_weight=0.5)
+    opt = torch.optim.Adam(obj.parameters(), lr=2e-3)
+    losses = []
+    for _ in range(8):
+        loss, stats = obj.loss(CAL)
+        opt.zero_grad()
+        loss.backward()
+        opt.step()
+        losses.append(float(loss))
+    assert {"state_1", "state_3", "ce_1", "ce_3", "loss"} <= set(stats)
+    assert losses[-1] < losses[0]
+    with pytest.raises(eco.ConfigError):
+        OBJECTIVES.get("jump_rollout")(em, horizon=0)
