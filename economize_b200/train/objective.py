@@ -240,10 +240,11 @@ def torch_block(layer, h: torch.Tensor, config, cos: torch.Tensor, sin: torch.Te
     x = rmsnorm(h, layer.mlp_norm, eps)[0]
     g, u = lin(x, layer.w_gate_up).chunk(2, -1)
     a = F.silu(g) * u
-    if getattr(layer, "down_hadamard", 0):  # the online rotation the rotate technique folded into w_down
+    block = getattr(layer, "down_hadamard", 0)  # the online rotation the rotate technique folded into w_down
+    if block:
         from ..ops import reference
 
-        a = reference.hadamard(a, getattr(layer, "down_hadamard"))
+        a = reference.hadamard(a, block)
     return h + lin(a, layer.w_down)
 
 
