@@ -104,9 +104,14 @@ def _worker(rank, world, port, queue):
             tree = em.decode_batch(prompts, 16, decoding=eco.DecodeConfig(
                 cycle_length=7, draft_policy="dynamic_tree", cuda_graphs=True,
                 draft_policy_options={"depth": 6, "topk": 10, "total_tokens": 60}))
-            # the sharded verification pass reduces every row as a one-token pass does: lossless, bit for bit
-            result[f"tp_fused{fused}_tree_equals_plain"] = all(torch.equal(a.tokens, b.tokens)
-                                                               for a, b in zip(tree, out))
+            # the fused path reduces the ranks' partials in rank order for every row count, so the sharded
+            # verification pass rounds as a one-token pass does: lossless, bit for bit. NCCL picks its reduction
+            # order per message size; with two ranks the sum does not depend on it, with more a 61-row pass may round
+            # otherwise than a one-row pass, so there the tree's tokens are checked for greedy validity below
+            exact_order = fused or world == 2
+            if exact_order:
+                result[f"tp_fused{fused}_tree_equals_plain"] = all(torch.equal(a.tokens, b.tokens)
+                                                                   for a, b in zip(tree, out))
             toks = torch.stack([r.tokens for r in out]).to(dev)
             every = [torch.empty_like(toks) for _ in range(world)]
             dist.all_gather(every, toks)
@@ -115,7 +120,8 @@ def _worker(rank, world, port, queue):
             # random model may take another greedy path; every token must be greedy (within a rounding-sized logit
             # gap) under the one-device model's causal recompute of the generated sequence, and the first agree
             greedy = True
-            for p, r in zip(prompts, out):
+            checked = list(zip(prompts, out)) + ([] if exact_order else list(zip(prompts, tree)))
+            for p, r in checked:
                 seq = torch.cat([p, r.tokens.to(dev)])
                 logits = ref_em(seq[None])[0].float()
                 for i, tok in enumerate(r.tokens.tolist()):
