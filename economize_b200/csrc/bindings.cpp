@@ -473,6 +473,7 @@ Tensor hadamard(Tensor x, int64_t block) {
   TORCH_CHECK(x.scalar_type() == at::kBFloat16, "hadamard: bf16 input");
   c10::cuda::CUDAGuard guard(x.device());
   x = x.contiguous();
+  if (reinterpret_cast<uintptr_t>(x.data_ptr()) % 16 != 0) x = x.clone();  // the kernel loads 16-byte vectors
   const int F = static_cast<int>(x.size(-1));
   const int rows = F ? static_cast<int>(x.numel() / F) : 0;
   auto out = at::empty_like(x);
@@ -490,6 +491,7 @@ Tensor glu_hadamard(Tensor gu, int64_t act, double limit, int64_t block) {
   CHECK_CUDA(gu);
   c10::cuda::CUDAGuard guard(gu.device());
   gu = gu.contiguous();
+  if (reinterpret_cast<uintptr_t>(gu.data_ptr()) % 16 != 0) gu = gu.clone();  // 16-byte vector loads
   auto [splits, shape] = parts_of(gu);
   const int F2 = static_cast<int>(shape.back());
   int64_t numel = 1;

@@ -70,3 +70,13 @@ def test_rotated_model_keeps_its_function_on_gpu(cuda):
     out = rot(ids).float()
     assert (out - base).norm() / base.norm() < 0.05
     assert (out.argmax(-1) == base.argmax(-1)).float().mean() > 0.9
+
+
+def test_hadamard_of_a_misaligned_view(cuda):
+    buf = torch.randn(3 * 64 + 1, device=cuda).bfloat16()
+    x = buf[1:].view(3, 64)  # contiguous, 2 bytes past a 16-byte boundary
+    assert x.data_ptr() % 16 != 0
+    torch.testing.assert_close(ops.hadamard(x, 64).float(), ref.hadamard(x.float(), 64), atol=2e-2, rtol=1e-2)
+    gu = torch.randn(2 * 2 * 64 + 1, device=cuda).bfloat16()[1:].view(2, 128)
+    want = ref.hadamard(ref.glu(gu.float(), "silu"), 64)
+    torch.testing.assert_close(ops.glu(gu, "silu", hadamard=64).float(), want, atol=3e-2, rtol=2e-2)
