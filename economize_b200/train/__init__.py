@@ -9,8 +9,9 @@ from .config import TrainConfig
 from .data import TensorSource, greedy_continuations
 from .loop import TrainResult, fit
 from .objective import OBJECTIVES, Eagle3TTT, Objective, OptimDefaults, default_objective, teacher_pass
+from .teacher import larger_teacher
 
-__all__ = ["OBJECTIVES", "Eagle3TTT", "Objective", "OptimDefaults", "RunCheckpointer", "TensorSource",
+__all__ = ["larger_teacher", "OBJECTIVES", "Eagle3TTT", "Objective", "OptimDefaults", "RunCheckpointer", "TensorSource",
            "TrainConfig", "TrainResult", "default_objective", "fit", "fit_eagle3_on_greedy", "greedy_continuations",
            "teacher_pass"]
 

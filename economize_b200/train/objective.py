@@ -335,16 +335,17 @@ def divergence(student_logp: torch.Tensor, teacher_p: torch.Tensor, kind: str) -
     raise ConfigError(f"unknown divergence {kind!r}; choose from {DIVERGENCES}")
 
 
-def _teacher_draft_probs(model, tech, tokens: torch.Tensor, top_k: int | None):
+def _teacher_draft_probs(model, tech, tokens: torch.Tensor, top_k: int | None, teacher=None):
     """Teacher next-token probabilities over the EAGLE-3 draft vocabulary ``[B, S, V_d]`` (restricted to the
-    teacher's ``top_k`` tokens when given), plus the captured block outputs."""
+    teacher's ``top_k`` tokens when given), plus the captured block outputs. ``teacher``: a function of the tokens
+    giving another model's logits (:func:`~economize_b200.train.teacher.larger_teacher`); ``None``: the target's."""
     target = model.model
     batch, length = tokens.shape
     cache = target.new_cache(batch, ((length + 127) // 128) * 128)
     lengths = torch.full((batch,), length, dtype=torch.int32, device=tokens.device)
     with torch.no_grad():
         hidden, aux = target.forward_step(tokens, StepBatch.prefill(lengths, length), cache, tech.aux_layers)
-        logits = target.logits(hidden).float()
+        logits = target.logits(hidden).float() if teacher is None else teacher(tokens)
         ids = torch.arange(tech.d2t.numel(), device=tokens.device) + tech.d2t
         drafted = logits[..., ids]  # the draft vocabulary's logits, draft order
         if top_k is not None:
@@ -357,13 +358,14 @@ def _teacher_draft_probs(model, tech, tokens: torch.Tensor, top_k: int | None):
 @OBJECTIVES.register("distill_kl")
 class Eagle3Distill(Objective):
     """Unrolled EAGLE-3 steps trained against the target's full next-token distribution (restricted to the draft
-    vocabulary) under a divergence (``kl``, ``rkl``, ``js``, ``tvd``, ``ce_top1``)."""
+    vocabulary) under a divergence (``kl``, ``rkl``, ``js``, ``tvd``, ``ce_top1``); ``teacher``: a larger model
+    with the same tokenizer (or its logits function) whose distributions replace the target's."""
 
     name = "distill_kl"
     defaults = OptimDefaults(lr=1e-3, warmup_steps=10)
 
     def __init__(self, model, divergence: str = "kl", steps: int | None = None, decay: float = 0.8,
-                 top_k: int | None = None) -> None:
+                 top_k: int | None = None, teacher=None) -> None:
         super().__init__(model)
         if "eagle3" not in model.techniques:
             raise ConfigError(f"{self.name} needs an attached eagle3 technique")
@@ -371,6 +373,11 @@ class Eagle3Distill(Objective):
             raise ConfigError(f"unknown divergence {divergence!r}")
         self.tech = model.techniques["eagle3"]
         self.kind, self.decay, self.top_k = divergence, decay, top_k
+        if isinstance(teacher, torch.nn.Module):  # a larger model with the same tokenizer
+            from .teacher import larger_teacher
+
+            teacher = larger_teacher(teacher, model.model.config.vocab_size)
+        self.teacher = teacher
         self.steps = steps or self.tech.config.train_steps
 
     def parameters(self) -> list[torch.nn.Parameter]:
@@ -379,7 +386,7 @@ class Eagle3Distill(Objective):
     def loss(self, tokens: torch.Tensor) -> tuple[torch.Tensor, dict[str, float]]:
         from ..techniques.eagle3.train import unrolled_logits
 
-        aux, probs = _teacher_draft_probs(self.model, self.tech, tokens, self.top_k)
+        aux, probs = _teacher_draft_probs(self.model, self.tech, tokens, self.top_k, self.teacher)
         outs = unrolled_logits(self.tech, aux, tokens, self.steps)
         positions = torch.arange(tokens.shape[1], device=tokens.device)
         total, weight, metrics = 0.0, 0.0, {}

@@ -173,3 +173,38 @@ def test_rl_building_blocks():
     assert abs(float(acceptance(p, torch.tensor([0.0, 0.0, 1.0]))) - 0.2) < 1e-7
     a = torch.full((4,), 0.6)
     assert abs(float(expected_tokens(a)) - (1 - 0.6 ** 5) / (1 - 0.6)) < 1e-5
+
+
+def test_distill_from_a_larger_teacher():
+    """distill_kl with a larger teacher: the distributions are the teacher's (same tokenizer), the drafter's inputs
+    the target's, and the loss goes down."""
+    from economize_b200.models.config import tiny_llama
+    from economize_b200.models.llama import CausalLM, init_weights
+    from economize_b200.techniques.eagle3 import Eagle3Config
+    from economize_b200.train import larger_teacher
+    from economize_b200.train.objective import OBJECTIVES, _teacher_draft_probs
+
+    from .helpers import tiny_model
+
+    big = init_weights(CausalLM(tiny_llama(num_layers=6, hidden_size=384, num_heads=6, num_kv_heads=2,
+                                           intermediate_size=1024), torch.float32, "cpu"), seed=5)
+    em = eco.apply(tiny_model(), Eagle3Config(draft_vocab=512))
+    tokens = torch.randint(0, 1024, (2, 24), generator=torch.Generator().manual_seed(2))
+    obj = OBJECTIVES.get("distill_kl")(em, teacher=big)
+    _, probs = _teacher_draft_probs(em, obj.tech, tokens, None, obj.teacher)
+    ids = torch.arange(obj.tech.d2t.numel()) + obj.tech.d2t
+    want = torch.softmax(larger_teacher(big)(tokens)[..., ids], -1)
+    torch.testing.assert_close(probs, want)
+    _, own = _teacher_draft_probs(em, obj.tech, tokens, None)
+    assert (own - probs).abs().max() > 1e-3  # not the target's distributions
+    opt = torch.optim.Adam(obj.parameters(), lr=2e-3)
+    losses = []
+    for _ in range(6):
+        loss, _ = obj.loss(tokens)
+        opt.zero_grad()
+        loss.backward()
+        opt.step()
+        losses.append(float(loss))
+    assert losses[-1] < losses[0]
+    with pytest.raises(eco.ConfigError, match="smaller"):
+        larger_teacher(big, vocab_size=4096)(tokens)
