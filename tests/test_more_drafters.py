@@ -252,3 +252,27 @@ def test_jump_open_loop_objective_trains():
     assert losses[-1] < losses[0]
     with pytest.raises(eco.ConfigError):
         OBJECTIVES.get("jump_rollout")(em, horizon=0)
+
+
+def test_jump_rl_pieces():
+    """Acceptances lie in [0, 1] and equal sum min(p, q) of the rollout's distributions; hybrid log-probabilities
+    take the target's distribution at cycle starts and the drafter's elsewhere, with gradients to the drafter."""
+    from economize_b200.techniques.jump.rl import hybrid_log_probs, jump_acceptance
+
+    em = eco.apply(tiny_model(), JumpConfig(target_layer=1, source_layer=2))
+    tech = em.techniques["jump"]
+    tokens = torch.randint(0, 1024, (2, 20), generator=torch.Generator().manual_seed(4))
+    acc = jump_acceptance(tech, tokens, 3)
+    assert acc.shape == (2, 17, 3) and bool(((acc >= 0) & (acc <= 1 + 1e-5)).all())
+    lp = hybrid_log_probs(tech, tokens, first=8, cycle_length=4)
+    assert lp.shape == (2, 12) and bool((lp <= 0).all())
+    with torch.no_grad():
+        exact = torch.log_softmax(em(tokens).float(), -1)
+    for i in (0, 4, 8):  # cycle starts: the target's own log-probabilities
+        t = 8 + i
+        torch.testing.assert_close(lp[:, i], exact[:, t - 1].gather(-1, tokens[:, t:t + 1])[:, 0], atol=1e-4,
+                                   rtol=1e-4)
+    lp.sum().backward()
+    assert tech.predictor.w2.weight.grad is not None and tech.predictor.w2.weight.grad.abs().sum() > 0
+    with pytest.raises(eco.ConfigError):
+        hybrid_log_probs(tech, tokens, first=8, cycle_length=1)
