@@ -12,6 +12,8 @@ peaks. Ops:
   counts); one JSON line per shape
 * ``gemm_wq``    weight-only int2 / int4 / int8 / fp8 / mxfp4 / nvfp4 GEMM (``--fmt``), vs the bf16 kernel on the
   same shape
+* ``hadamard``   SwiGLU with the online Hadamard rotation fused (block ``--group``, width ``--n``) vs the plain
+  SwiGLU kernel on the same input
 * ``attention``  tree-masked decode attention over a bf16 slot cache (``--tree`` new tokens per row)
 * ``layer``      one Llama-3.1-8B decoder layer's projections as a CUDA graph (``--tp`` shard), ours vs cuBLAS
 * ``teal``       activation-sparse GEMV (``colsparse_linear`` over a transposed weight) at ``--sparsity`` of the
@@ -315,9 +317,31 @@ def bench_glu(a) -> None:
             nbytes, 2 * a.m * F_ * H * kept, dense)
 
 
+def bench_hadamard(a) -> None:
+    """The gated activation with the online Hadamard rotation fused (``glu_hadamard``) against the plain gated
+    activation (``silu_mul``) of the same ``[M, 2F]`` input, inputs rotated over copies larger than L2."""
+    from ..ops._ext import require
+
+    dev = torch.device("cuda")
+    C = require()
+    F_ = a.n
+    block = a.group if a.group >= 8 else 2048
+    n_copies = 1 if a.once else _copies(4 * a.m * F_)
+    gus = [torch.randn(a.m, 2 * F_, device=dev).bfloat16() for _ in range(n_copies)]
+    if a.once:
+        C.glu_hadamard(gus[0], 0, 7.0, block)
+        torch.cuda.synchronize()
+        return
+    fused = time_graph([lambda g=g: C.glu_hadamard(g, 0, 7.0, block) for g in gus], a.iters, a.warmup)
+    plain = time_graph([lambda g=g: C.silu_mul(g) for g in gus], a.iters, a.warmup)
+    _report("glu_hadamard", {"M": a.m, "F": F_, "block": block}, fused, 2 * (2 * a.m * F_ + a.m * F_),
+            a.m * F_ * (block.bit_length() - 1), plain)
+
+
 def main(argv: list[str] | None = None) -> None:
     p = argparse.ArgumentParser(description=__doc__.splitlines()[0])
-    p.add_argument("op", choices=["gemm", "gemm_sweep", "gemm_wq", "attention", "layer", "teal", "glu", "topk"])
+    p.add_argument("op", choices=["gemm", "gemm_sweep", "gemm_wq", "attention", "layer", "teal", "glu", "topk",
+                                  "hadamard"])
     p.add_argument("--ms", type=int, nargs="+", default=[1, 8, 61, 488], help="gemm_sweep: token counts")
     p.add_argument("--topk", type=int, default=10)
     p.add_argument("--m", type=int, default=61)
@@ -338,7 +362,7 @@ def main(argv: list[str] | None = None) -> None:
     p.add_argument("--trace", action="store_true", help="attention: per-CTA phase timeline from the kernel's stamps")
     a = p.parse_args(argv)
     {"gemm": bench_gemm, "gemm_sweep": bench_gemm_sweep, "gemm_wq": bench_gemm_wq, "attention": bench_attention, "layer": bench_layer,
-     "teal": bench_teal, "glu": bench_glu, "topk": bench_topk}[a.op](a)
+     "teal": bench_teal, "glu": bench_glu, "topk": bench_topk, "hadamard": bench_hadamard}[a.op](a)
 
 
 if __name__ == "__main__":
