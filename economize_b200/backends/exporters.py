@@ -100,3 +100,12 @@ def export_drafter(model: Any, path: str | Path, *, backend: str, technique: str
     """Write ``model``'s drafter as the draft-model folder ``backend`` loads; returns the folder."""
     exporter, instance = exporter_for(model, backend, technique)
     return exporter.export(instance, path, **options)
+
+
+def refuse_online_rotation(target, fmt: str) -> None:
+    """Refuse to write a model whose down projections expect an online Hadamard rotation of their input (the
+    ``rotate`` technique's ``online`` option): ``fmt`` files carry no such transform, so they would compute another
+    function."""
+    if any(getattr(layer, "down_hadamard", 0) for layer in target.layers):
+        raise ConfigError(f"{fmt} files carry no online Hadamard rotation; export the model before rotate, or rotate "
+                          "with online=()")

@@ -63,6 +63,9 @@ def to_mlx(model, folder: str | Path, dtype: torch.dtype = torch.bfloat16) -> Pa
     from safetensors.torch import save_file
 
     target = getattr(model, "model", model)
+    from .exporters import refuse_online_rotation
+
+    refuse_online_rotation(target, "mlx_lm")
     c = target.config
     folder = Path(folder)
     folder.mkdir(parents=True, exist_ok=True)

@@ -69,6 +69,9 @@ def to_trtllm(model, folder: str | Path, tp: int = 1, dtype: torch.dtype = torch
     from safetensors.torch import save_file
 
     target = getattr(model, "model", model)
+    from .exporters import refuse_online_rotation
+
+    refuse_online_rotation(target, "TensorRT-LLM")
     c = target.config
     if c.is_moe or c.post_norm or c.sandwich_norm or c.hidden_act != "silu" or c.qk_norm or c.attention_bias:
         raise ConfigError("the TensorRT-LLM writer covers the plain Llama block")

@@ -113,6 +113,9 @@ def _linear_entries(qw: QWeight, prefix: str) -> tuple[dict[str, torch.Tensor], 
 def export_compressed_tensors(model, path: str | Path) -> Path:
     """Write ``model``'s target (an EfficientModel or CausalLM whose projections the ``quant`` technique replaced)
     as a compressed-tensors folder; returns the folder."""
+    from ..backends.exporters import refuse_online_rotation
+
+    refuse_online_rotation(getattr(model, "model", model), "compressed-tensors")
     from safetensors.torch import save_file
 
     lm = getattr(model, "model", model)

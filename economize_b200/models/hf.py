@@ -185,7 +185,7 @@ def export_hf_state(model, copy: bool = True) -> dict[str, torch.Tensor]:
                 out[p + "mlp.shared_expert_gate.weight"] = layer.shared_gate.detach()
         elif c.model_type == "phi3":
             out[p + "mlp.gate_up_proj.weight"] = full(layer.w_gate_up)
-            out[p + "mlp.down_proj.weight"] = full(layer.w_down)
+            out[p + "mlp.down_proj.weight"] = _unrotated_down(layer, full(layer.w_down))
         else:
             g, u = full(layer.w_gate_up).chunk(2, 0)
             out[p + "mlp.gate_proj.weight"] = g

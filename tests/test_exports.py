@@ -4,6 +4,7 @@ weights (dequantized codes equal the engine's), and the configs name the archite
 import json
 
 import numpy as np
+import pytest
 import torch
 from safetensors.torch import load_file
 
@@ -68,3 +69,18 @@ def test_trtllm_checkpoint_names_shards_and_awq_codes(tmp_path):
         torch.testing.assert_close(signed * scales, dense[:, r * k:(r + 1) * k], atol=1e-3, rtol=1e-3)
         assert state[p + "attention.qkv.weight"].shape[0] == (c.q_size + 2 * c.kv_size) // 2 // 2  # rows / 2 / tp
         assert state[p + "mlp.proj.weight"].shape == (c.hidden_size, c.intermediate_size // 2)  # dense (K 688)
+
+
+def test_exports_refuse_an_online_rotation(tmp_path):
+    import economize_b200 as eco
+    from economize_b200.backends.mlx import to_mlx
+    from economize_b200.backends.trtllm import to_trtllm
+    from economize_b200.integrations.compressed_tensors import export_compressed_tensors
+    from economize_b200.techniques.rotate import RotateConfig
+
+    from .helpers import tiny_model
+
+    em = eco.apply(tiny_model(), RotateConfig())
+    for write in (to_mlx, to_trtllm, export_compressed_tensors):
+        with pytest.raises(eco.ConfigError, match="online Hadamard"):
+            write(em, tmp_path / write.__name__)
